@@ -1,0 +1,35 @@
+// Host interface of the paged attention kernels (paged_attention.cu).
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+namespace b200 {
+
+struct PagedAttnParams {
+  const __nv_bfloat16* q;  // [T, Hq, D] (token stride q_stride_t)
+  long long q_stride_t;
+  const __nv_bfloat16* k_cache;  // [num_blocks, Hkv, block_size, D]
+  const __nv_bfloat16* v_cache;
+  long long kv_block_stride;     // elements between consecutive blocks
+  const int* block_tables;       // [B, bt_stride]
+  int bt_stride;
+  const int* seq_lens;           // [B] total KV length (cached + this step)
+  const int* q_start;            // [B + 1] cumulative query lengths
+  const int2* work;              // [num_work] (sequence, first packed row)
+  __nv_bfloat16* out;            // [T, Hq, D]
+  long long o_stride_t;
+  float* part_o;                 // [splits, T, Hq, D] (split-KV only)
+  float* part_lse;               // [splits, T, Hq]
+  const float* sinks;            // [Hq] or null
+  int num_splits;
+  int Hq, Hkv, G;
+  int block_size;
+  int window;                    // 0 = full attention
+  float scale_log2;              // softmax scale * log2(e)
+  int total_tokens;
+};
+
+void paged_attention_launch(const PagedAttnParams& p, int num_work, int head_dim, bool decode,
+                            cudaStream_t stream);
+
+}  // namespace b200

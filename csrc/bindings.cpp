@@ -1,0 +1,275 @@
+// Python bindings of the sm_100a kernels.  Every op launches on the caller's current CUDA
+// stream and allocates nothing (outputs and scratch are passed in), so the calls can be
+// recorded into CUDA graphs.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <mutex>
+#include <unordered_map>
+
+#include "attn/attention.h"
+#include "gemm/gemm.h"
+#include "misc/misc.h"
+
+namespace {
+
+#define CHECK_CUDA(x) TORCH_CHECK((x).is_cuda(), #x " must be a CUDA tensor")
+#define CHECK_BF16(x) TORCH_CHECK((x).scalar_type() == at::kBFloat16, #x " must be bfloat16")
+
+cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+// One status word per device; kernels record bounded-wait failures into it.
+uint32_t* status_word() {
+  static std::mutex mu;
+  static std::unordered_map<int, uint32_t*> words;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> g(mu);
+  auto it = words.find(dev);
+  if (it != words.end()) return it->second;
+  uint32_t* p = nullptr;
+  TORCH_CHECK(cudaMalloc(&p, sizeof(uint32_t)) == cudaSuccess, "status word allocation failed");
+  TORCH_CHECK(cudaMemset(p, 0, sizeof(uint32_t)) == cudaSuccess, "status word init failed");
+  words[dev] = p;
+  return p;
+}
+
+int64_t read_status() {
+  uint32_t v = 0;
+  TORCH_CHECK(cudaMemcpy(&v, status_word(), sizeof(v), cudaMemcpyDeviceToHost) == cudaSuccess);
+  return v;
+}
+void reset_status() { TORCH_CHECK(cudaMemset(status_word(), 0, sizeof(uint32_t)) == cudaSuccess); }
+
+void check_launch(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  TORCH_CHECK(e == cudaSuccess, what, " launch failed: ", cudaGetErrorString(e));
+}
+
+// out = A @ B^T with the given epilogue.  A [M, K], B [N, K], both K-contiguous bf16.
+void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, int64_t epi, int64_t bn,
+          int64_t splits, int64_t group_m, int64_t max_ctas) {
+  CHECK_CUDA(a);
+  CHECK_CUDA(b);
+  CHECK_CUDA(out);
+  CHECK_BF16(a);
+  CHECK_BF16(b);
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.size(1) == b.size(1), "gemm: bad shapes");
+  TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1 && out.stride(-1) == 1,
+              "gemm: inner dims must be contiguous");
+  const bool f32_out = (epi == b200::EPI_F32_RED || epi == b200::EPI_F32_RED_T);
+  TORCH_CHECK(out.scalar_type() == (f32_out ? at::kFloat : at::kBFloat16), "gemm: out dtype");
+  const c10::cuda::CUDAGuard guard(a.device());
+  b200::GemmArgs g{};
+  g.A = a.data_ptr();
+  g.B = b.data_ptr();
+  g.out = out.data_ptr();
+  g.lda = a.stride(0);
+  g.ldb = b.stride(0);
+  g.ldo = out.stride(0);
+  g.M = (int)a.size(0);
+  g.N = (int)b.size(0);
+  g.K = (int)a.size(1);
+  g.bn = (int)bn;
+  g.epi = (int)epi;
+  g.splits = (int)splits;
+  g.group_m = (int)group_m;
+  g.max_ctas = (int)max_ctas;
+  g.status = status_word();
+  if (g.M == 0 || g.N == 0) return;
+  b200::gemm_bf16_launch(g, cur_stream());
+  check_launch("gemm");
+}
+
+void paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
+                     const at::Tensor& block_tables, const at::Tensor& seq_lens,
+                     const at::Tensor& q_start, const at::Tensor& work, at::Tensor& out,
+                     c10::optional<at::Tensor> part_o, c10::optional<at::Tensor> part_lse,
+                     c10::optional<at::Tensor> sinks, int64_t num_splits, int64_t num_kv_heads,
+                     int64_t window, double scale, bool decode) {
+  CHECK_CUDA(q);
+  CHECK_BF16(q);
+  CHECK_BF16(k_cache);
+  TORCH_CHECK(q.dim() == 3, "q must be [T, Hq, D]");
+  TORCH_CHECK(k_cache.dim() == 4, "k_cache must be [num_blocks, Hkv, block_size, D]");
+  TORCH_CHECK(block_tables.scalar_type() == at::kInt && seq_lens.scalar_type() == at::kInt &&
+                  q_start.scalar_type() == at::kInt && work.scalar_type() == at::kInt,
+              "metadata must be int32");
+  TORCH_CHECK(q.stride(2) == 1 && q.stride(1) == q.size(2), "q heads must be packed");
+  TORCH_CHECK(out.stride(2) == 1 && out.stride(1) == out.size(2), "out heads must be packed");
+  const c10::cuda::CUDAGuard guard(q.device());
+  b200::PagedAttnParams p{};
+  const int D = (int)q.size(2);
+  p.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  p.q_stride_t = q.stride(0);
+  p.k_cache = reinterpret_cast<const __nv_bfloat16*>(k_cache.data_ptr());
+  p.v_cache = reinterpret_cast<const __nv_bfloat16*>(v_cache.data_ptr());
+  p.kv_block_stride = k_cache.stride(0);
+  TORCH_CHECK(v_cache.stride(0) == k_cache.stride(0), "k/v cache strides differ");
+  p.block_tables = block_tables.data_ptr<int>();
+  p.bt_stride = (int)block_tables.stride(0);
+  p.seq_lens = seq_lens.data_ptr<int>();
+  p.q_start = q_start.data_ptr<int>();
+  p.work = reinterpret_cast<const int2*>(work.data_ptr<int>());
+  p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  p.o_stride_t = out.stride(0);
+  p.num_splits = (int)num_splits;
+  if (num_splits > 1) {
+    TORCH_CHECK(part_o.has_value() && part_lse.has_value(), "split-KV needs partial buffers");
+    TORCH_CHECK(part_o->numel() >= num_splits * q.size(0) * q.size(1) * D, "part_o too small");
+    p.part_o = part_o->data_ptr<float>();
+    p.part_lse = part_lse->data_ptr<float>();
+  }
+  p.sinks = sinks.has_value() ? sinks->data_ptr<float>() : nullptr;
+  p.Hq = (int)q.size(1);
+  p.Hkv = (int)num_kv_heads;
+  p.G = p.Hq / p.Hkv;
+  p.block_size = (int)k_cache.size(2);
+  p.window = (int)window;
+  p.scale_log2 = (float)(scale * 1.4426950408889634);
+  p.total_tokens = (int)q.size(0);
+  const int num_work = (int)work.size(0);
+  b200::paged_attention_launch(p, num_work, D, decode, cur_stream());
+  check_launch("paged_attention");
+}
+
+void add_rmsnorm(at::Tensor& x, c10::optional<at::Tensor> residual, const at::Tensor& w,
+                 at::Tensor& out, double eps, bool clear_x) {
+  CHECK_CUDA(x);
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int rows = (int)x.size(0), H = (int)x.size(1);
+  TORCH_CHECK(x.stride(1) == 1 && out.stride(1) == 1, "rows must be contiguous");
+  __nv_bfloat16* res = nullptr;
+  long long rs = 0;
+  if (residual.has_value()) {
+    CHECK_BF16(*residual);
+    res = reinterpret_cast<__nv_bfloat16*>(residual->data_ptr());
+    rs = residual->stride(0);
+  }
+  b200::add_rmsnorm_launch(x.data_ptr(), x.scalar_type() == at::kFloat, x.stride(0), res, rs,
+                           reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
+                           reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0), rows,
+                           H, (float)eps, clear_x, cur_stream());
+  check_launch("add_rmsnorm");
+}
+
+void rope_kv_write(at::Tensor& qkv, const at::Tensor& positions,
+                   c10::optional<at::Tensor> slot_mapping, const at::Tensor& cos_sin,
+                   at::Tensor& q_out, c10::optional<at::Tensor> k_cache,
+                   c10::optional<at::Tensor> v_cache, c10::optional<at::Tensor> q_norm_w,
+                   c10::optional<at::Tensor> k_norm_w, double eps, int64_t num_q_heads,
+                   int64_t num_kv_heads, int64_t head_dim, int64_t rot_dim, bool neox,
+                   bool clear_input) {
+  CHECK_CUDA(qkv);
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  b200::RopeKvParams p{};
+  p.positions = positions.data_ptr<int>();
+  p.slot_mapping = slot_mapping.has_value()
+                       ? reinterpret_cast<const long long*>(slot_mapping->data_ptr<int64_t>())
+                       : nullptr;
+  p.cos_sin = cos_sin.data_ptr<float>();
+  p.qkv_stride = qkv.stride(0);
+  p.q_out = reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr());
+  p.q_out_stride = q_out.stride(0);
+  if (k_cache.has_value()) {
+    p.k_cache = reinterpret_cast<__nv_bfloat16*>(k_cache->data_ptr());
+    p.v_cache = reinterpret_cast<__nv_bfloat16*>(v_cache->data_ptr());
+    p.kv_block_stride = k_cache->stride(0);
+    p.block_size = (int)k_cache->size(2);
+  } else {
+    p.slot_mapping = nullptr;
+    p.block_size = 1;
+  }
+  p.q_norm_w = q_norm_w.has_value() ? reinterpret_cast<const __nv_bfloat16*>(q_norm_w->data_ptr()) : nullptr;
+  p.k_norm_w = k_norm_w.has_value() ? reinterpret_cast<const __nv_bfloat16*>(k_norm_w->data_ptr()) : nullptr;
+  p.eps = (float)eps;
+  p.Hq = (int)num_q_heads;
+  p.Hkv = (int)num_kv_heads;
+  p.head_dim = (int)head_dim;
+  p.rot_dim = (int)rot_dim;
+  p.neox = neox;
+  p.clear_input = clear_input;
+  b200::rope_kv_write_launch(p, qkv.data_ptr(), qkv.scalar_type() == at::kFloat,
+                             (int)qkv.size(0), cur_stream());
+  check_launch("rope_kv_write");
+}
+
+void silu_mul(at::Tensor& inp, at::Tensor& out, int64_t blk, bool clear_input, int64_t act,
+              double limit, double alpha) {
+  CHECK_CUDA(inp);
+  const c10::cuda::CUDAGuard guard(inp.device());
+  const int T = (int)inp.size(0), I = (int)out.size(1);
+  TORCH_CHECK(inp.size(1) == 2 * I, "silu_mul: input must have 2 * I columns");
+  b200::silu_mul_launch(inp.data_ptr(), inp.scalar_type() == at::kFloat, inp.stride(0),
+                        reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0), T, I,
+                        (int)blk, clear_input, (int)act, (float)limit, (float)alpha,
+                        cur_stream());
+  check_launch("silu_mul");
+}
+
+void embedding(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out,
+               int64_t vocab_start, int64_t vocab_end) {
+  CHECK_CUDA(ids);
+  TORCH_CHECK(ids.scalar_type() == at::kInt, "ids must be int32");
+  const c10::cuda::CUDAGuard guard(ids.device());
+  b200::embedding_launch(ids.data_ptr<int>(), reinterpret_cast<const __nv_bfloat16*>(table.data_ptr()),
+                         reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), (int)ids.size(0),
+                         (int)table.size(1), (int)vocab_start, (int)vocab_end, cur_stream());
+  check_launch("embedding");
+}
+
+void sample(const at::Tensor& logits, const at::Tensor& temperature, const at::Tensor& top_k,
+            const at::Tensor& top_p, c10::optional<at::Tensor> min_p, const at::Tensor& seeds,
+            const at::Tensor& offsets, at::Tensor& out_tokens,
+            c10::optional<at::Tensor> out_logprob, int64_t vocab_offset) {
+  CHECK_CUDA(logits);
+  const c10::cuda::CUDAGuard guard(logits.device());
+  b200::SampleParams p{};
+  p.logits = logits.data_ptr();
+  p.logits_f32 = logits.scalar_type() == at::kFloat;
+  p.logits_stride = logits.stride(0);
+  p.B = (int)logits.size(0);
+  p.V = (int)logits.size(1);
+  p.temperature = temperature.data_ptr<float>();
+  p.top_k = top_k.data_ptr<int>();
+  p.top_p = top_p.data_ptr<float>();
+  p.min_p = min_p.has_value() ? min_p->data_ptr<float>() : nullptr;
+  p.seeds = reinterpret_cast<const uint64_t*>(seeds.data_ptr<int64_t>());
+  p.offsets = offsets.data_ptr<int>();
+  p.out_tokens = out_tokens.data_ptr<int>();
+  p.out_logprob = out_logprob.has_value() ? out_logprob->data_ptr<float>() : nullptr;
+  p.vocab_offset = (int)vocab_offset;
+  b200::sample_launch(p, cur_stream());
+  check_launch("sample");
+}
+
+void argmax(const at::Tensor& logits, at::Tensor& out_idx, c10::optional<at::Tensor> out_val,
+            int64_t vocab_offset) {
+  CHECK_CUDA(logits);
+  const c10::cuda::CUDAGuard guard(logits.device());
+  b200::argmax_launch(logits.data_ptr(), logits.scalar_type() == at::kFloat, logits.stride(0),
+                      (int)logits.size(0), (int)logits.size(1), out_idx.data_ptr<int>(),
+                      out_val.has_value() ? out_val->data_ptr<float>() : nullptr,
+                      (int)vocab_offset, cur_stream());
+  check_launch("argmax");
+}
+
+int64_t num_sms() { return b200::num_sms_cached(); }
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "sm_100a kernels of vllm_neuron_b200";
+  m.def("gemm", &gemm);
+  m.def("paged_attention", &paged_attention);
+  m.def("add_rmsnorm", &add_rmsnorm);
+  m.def("rope_kv_write", &rope_kv_write);
+  m.def("silu_mul", &silu_mul);
+  m.def("embedding", &embedding);
+  m.def("sample", &sample);
+  m.def("argmax", &argmax);
+  m.def("read_status", &read_status);
+  m.def("reset_status", &reset_status);
+  m.def("num_sms", &num_sms);
+}

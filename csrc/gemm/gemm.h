@@ -1,0 +1,36 @@
+// Host interface of the sm_100a tcgen05 GEMM (gemm_sm100.cu).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace b200 {
+
+enum GemmEpilogue : int {
+  EPI_BF16 = 0,       // out[m, n] = D           (bf16)
+  EPI_BF16_T = 1,     // out[n, m] = D           (bf16, swapped operands)
+  EPI_F32_RED = 2,    // out[m, n] += D          (fp32 reduction, split-K)
+  EPI_F32_RED_T = 3,  // out[n, m] += D          (fp32 reduction, swapped operands)
+  EPI_SILU_BF16 = 4,  // out[m, j] = silu(gate) * up, gate/up interleaved per BN tile
+};
+
+struct GemmArgs {
+  const void* A;  // [M, K] bf16, row pitch lda
+  const void* B;  // [N, K] bf16, row pitch ldb
+  void* out;
+  long long lda, ldb, ldo;
+  int M, N, K;
+  int bn;         // N tile: 16/32/64/128/256
+  int epi;        // GemmEpilogue
+  int splits;     // split-K factor (needs an fp32 reduction epilogue when > 1)
+  int group_m;    // rasterization group along M (0 = default)
+  int max_ctas;   // cap on persistent CTAs (0 = number of SMs)
+  uint32_t* status;  // device status word for bounded-wait failures (may be null)
+};
+
+void gemm_bf16_launch(const GemmArgs& args, cudaStream_t stream);
+CUtensorMap make_tmap_bf16_2d(const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld,
+                              uint32_t box_inner, uint32_t box_outer, bool swizzle128);
+int num_sms_cached();
+
+}  // namespace b200

@@ -1,0 +1,433 @@
+// Persistent, warp-specialized bf16 GEMM for sm_100a on the 5th-generation tensor cores.
+//
+//   D[M, N] = A[M, K] * B[N, K]^T     (A and B K-contiguous, fp32 accumulation in TMEM)
+//
+// Roles (192 threads, one CTA per SM):
+//   warp 0      TMA producer: one elected thread streams 128x64 A tiles and BNx64 B tiles
+//               (128-byte swizzle) into a STAGES-deep shared-memory ring.
+//   warp 1      allocates TMEM (2 accumulator buffers of BN fp32 columns) and one elected
+//               thread issues tcgen05.mma (M=128, N=BN, K=16) and tcgen05.commit.
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator (one TMEM lane = one output row per
+//               thread), conversion and global stores, overlapped with the next tile's MMA.
+//
+// Epilogues:
+//   EPI_BF16      out[m, n]  (row-major, bf16)
+//   EPI_BF16_T    out[n, m]  (transposed store, used with swapped operands for skinny
+//                 decode batches: A = weight rows, B = tokens)
+//   EPI_F32_RED   out[m, n] += D (fp32 reductions; used for split-K)
+//   EPI_F32_RED_T out[n, m] += D
+//   EPI_SILU_BF16 out[m, j] = silu(D[m, g]) * D[m, u] where the weight rows of each BN tile
+//                 are [BN/2 gate rows | BN/2 up rows] (interleaved at load time)
+//
+// This is the B200 replacement of the dense projections that the reference runs through
+// its NKI qkv / mlp / output_projection kernels (vllm_neuron/functional/attention/qkv.py:672,
+// vllm_neuron/functional/mlp.py:65, vllm_neuron/functional/attention/o_proj.py:124).
+#include <cudaTypedefs.h>
+
+#include <cstdio>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+
+#include "../common.cuh"
+#include "gemm.h"
+
+namespace b200 {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;  // 64 bf16 = 128 bytes = one swizzle row
+constexpr int kATileBytes = kBM * kBK * 2;
+
+struct GemmParams {
+  int M, N, K;
+  int num_m_blocks, num_n_blocks, num_k_blocks;
+  int splits, kb_per_split;
+  int group_m;
+  void* out;
+  long long ldo;
+  uint32_t* status;
+};
+
+__device__ __forceinline__ void decode_tile(const GemmParams& p, int tile, int& mb, int& nb,
+                                            int& split) {
+  const int mn_tiles = p.num_m_blocks * p.num_n_blocks;
+  split = tile / mn_tiles;
+  const int mn = tile - split * mn_tiles;
+  const int group_size = p.group_m * p.num_n_blocks;
+  const int g = mn / group_size;
+  const int first_m = g * p.group_m;
+  const int gm = min(p.num_m_blocks - first_m, p.group_m);
+  const int r = mn - g * group_size;
+  mb = first_m + r % gm;
+  nb = r / gm;
+}
+
+template <int BN>
+struct TmemCols {
+  static constexpr int v = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128
+                           : (2 * BN <= 256) ? 256 : 512;
+};
+
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+
+template <int BN, int STAGES, int EPI>
+__global__ void __launch_bounds__(192, 1)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA,
+                     const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
+  constexpr int kBTileBytes = BN * kBK * 2;
+  constexpr int kStageBytes = kATileBytes + kBTileBytes;
+  constexpr uint32_t kTmemCols = TmemCols<BN>::v;
+  constexpr uint32_t kIdesc = make_idesc_f16(kBM, BN, true);
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 1024-byte alignment for the swizzled tiles.
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* smA = smem;
+  uint8_t* smB = smem + STAGES * kATileBytes;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * kStageBytes);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint32_t* tmem_base_smem = reinterpret_cast<uint32_t*>(tempty_bar + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_smem + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 4);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_base_smem, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_smem;
+
+  const int total_tiles = p.num_m_blocks * p.num_n_blocks * p.splits;
+
+  if (warp == 0) {
+    // ------------------------------ TMA producer ------------------------------
+    if (elect_one()) {
+      const uint64_t hint_a = (EPI == EPI_BF16_T || EPI == EPI_F32_RED_T)
+                                  ? policy_evict_first()  // A = weights, streamed once
+                                  : policy_evict_last();
+      const uint64_t hint_b = (EPI == EPI_BF16_T || EPI == EPI_F32_RED_T)
+                                  ? policy_evict_last()   // B = activations, reused
+                                  : policy_evict_first();
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+        int mb, nb, split;
+        decode_tile(p, tile, mb, nb, split);
+        const int k0 = split * p.kb_per_split;
+        const int k1 = min(k0 + p.kb_per_split, p.num_k_blocks);
+        for (int kb = k0; kb < k1; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait_abortable(&empty_bar[s], ph ^ 1, kTimeoutSmemEmpty, p.status, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full_bar[s], kStageBytes);
+          tma_load_2d(&tmA, &full_bar[s], smA + s * kATileBytes, kb * kBK, mb * kBM, hint_a);
+          tma_load_2d(&tmB, &full_bar[s], smB + s * kBTileBytes, kb * kBK, nb * BN, hint_b);
+        }
+      }
+      if (!ok) {
+        // Drain the copies still in flight before the CTA's shared memory is released.
+        const uint32_t first = it > (uint32_t)STAGES ? it - STAGES : 0;
+        for (uint32_t j = first; j < it; ++j)
+          mbar_wait(&full_bar[j % STAGES], (j / STAGES) & 1, kTimeoutTmaFull, p.status);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer ------------------------------
+    if (elect_one()) {
+      uint32_t it = 0;
+      int t_local = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x, ++t_local) {
+        int mb, nb, split;
+        decode_tile(p, tile, mb, nb, split);
+        const int k0 = split * p.kb_per_split;
+        const int k1 = min(k0 + p.kb_per_split, p.num_k_blocks);
+        const int acc = t_local & 1;
+        const uint32_t aph = (t_local >> 1) & 1;
+        if (!mbar_wait_abortable(&tempty_bar[acc], aph ^ 1, kTimeoutTmemEmpty, p.status, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = k0; kb < k1; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait_abortable(&full_bar[s], ph, kTimeoutTmaFull, p.status, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smA + s * kATileBytes);
+          const uint32_t b_addr = smem_u32(smB + s * kBTileBytes);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t adesc = make_sdesc_sw128(a_addr + k * 32);
+            const uint64_t bdesc = make_sdesc_sw128(b_addr + k * 32);
+            umma_f16_ss(d_tmem, adesc, bdesc, kIdesc, (kb > k0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty_bar[s]);
+        }
+        if (ok) umma_commit(&tfull_bar[acc]);
+      }
+    }
+  } else {
+    // ------------------------------ epilogue ------------------------------
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int row = q * 32 + lane;
+    int t_local = 0;
+    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++t_local) {
+      int mb, nb, split;
+      decode_tile(p, tile, mb, nb, split);
+      const int acc = t_local & 1;
+      const uint32_t aph = (t_local >> 1) & 1;
+      if (!mbar_wait_abortable(&tfull_bar[acc], aph, kTimeoutTmemFull, p.status, abort_flag)) break;
+      tc_fence_after();
+      const int m = mb * kBM + row;
+      const int n_base = nb * BN;
+      const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
+
+      if constexpr (EPI == EPI_SILU_BF16) {
+        // Tile columns [0, BN/2) are gate rows, [BN/2, BN) the matching up rows.
+        constexpr int H = BN / 2;
+        const int j_base = nb * H;  // output column base
+        const int n_out = p.N / 2;
+#pragma unroll 1
+        for (int c = 0; c < H; c += 16) {
+          uint32_t g[16], u[16];
+          tmem_ld_32x32b_x16(t_row + c, g);
+          tmem_ld_32x32b_x16(t_row + H + c, u);
+          tmem_ld_wait();
+          if (m < p.M) {
+            __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + (long long)m * p.ldo;
+            uint32_t packed[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float g0 = __uint_as_float(g[2 * j]), g1 = __uint_as_float(g[2 * j + 1]);
+              const float u0 = __uint_as_float(u[2 * j]), u1 = __uint_as_float(u[2 * j + 1]);
+              packed[j] = pack_bf16x2(silu_f(g0) * u0, silu_f(g1) * u1);
+            }
+            const int j0 = j_base + c;
+            if (j0 + 16 <= n_out && (p.ldo % 8) == 0) {
+              uint4* dst = reinterpret_cast<uint4*>(o + j0);
+              dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+              dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+            } else {
+              for (int j = 0; j < 16; ++j) {
+                if (j0 + j < n_out) {
+                  const float2 f = unpack_bf16x2(packed[j >> 1]);
+                  o[j0 + j] = __float2bfloat16((j & 1) ? f.y : f.x);
+                }
+              }
+            }
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_row + c, r);
+          tmem_ld_wait();
+          const int n0 = n_base + c;
+          if constexpr (EPI == EPI_BF16) {
+            if (m < p.M) {
+              __nv_bfloat16* o =
+                  reinterpret_cast<__nv_bfloat16*>(p.out) + (long long)m * p.ldo + n0;
+              if (n0 + 32 <= p.N && (p.ldo % 8) == 0) {
+                uint4* dst = reinterpret_cast<uint4*>(o);
+#pragma unroll
+                for (int v = 0; v < 4; ++v) {
+                  dst[v] = make_uint4(
+                      pack_bf16x2(__uint_as_float(r[8 * v + 0]), __uint_as_float(r[8 * v + 1])),
+                      pack_bf16x2(__uint_as_float(r[8 * v + 2]), __uint_as_float(r[8 * v + 3])),
+                      pack_bf16x2(__uint_as_float(r[8 * v + 4]), __uint_as_float(r[8 * v + 5])),
+                      pack_bf16x2(__uint_as_float(r[8 * v + 6]), __uint_as_float(r[8 * v + 7])));
+                }
+              } else {
+                for (int j = 0; j < 32; ++j)
+                  if (n0 + j < p.N) o[j] = __float2bfloat16(__uint_as_float(r[j]));
+              }
+            }
+          } else if constexpr (EPI == EPI_BF16_T) {
+            if (m < p.M) {
+              __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + m;
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (n0 + j < p.N)
+                  o[(long long)(n0 + j) * p.ldo] = __float2bfloat16(__uint_as_float(r[j]));
+            }
+          } else if constexpr (EPI == EPI_F32_RED) {
+            if (m < p.M) {
+              float* o = reinterpret_cast<float*>(p.out) + (long long)m * p.ldo + n0;
+              if (n0 + 32 <= p.N && (p.ldo % 4) == 0) {
+#pragma unroll
+                for (int v = 0; v < 8; ++v)
+                  atomicAdd(reinterpret_cast<float4*>(o) + v,
+                            make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                        __uint_as_float(r[4 * v + 2]),
+                                        __uint_as_float(r[4 * v + 3])));
+              } else {
+                for (int j = 0; j < 32; ++j)
+                  if (n0 + j < p.N) atomicAdd(o + j, __uint_as_float(r[j]));
+              }
+            }
+          } else {  // EPI_F32_RED_T
+            if (m < p.M) {
+              float* o = reinterpret_cast<float*>(p.out) + m;
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (n0 + j < p.N) atomicAdd(o + (long long)(n0 + j) * p.ldo, __uint_as_float(r[j]));
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// Host side
+// ------------------------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || ptr == nullptr)
+      throw std::runtime_error("cuTensorMapEncodeTiled is not available from the driver");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// 2D bf16 tensor [outer, inner] with row pitch `ld` elements; box = [box_outer, box_inner].
+CUtensorMap make_tmap_bf16_2d(const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld,
+                              uint32_t box_inner, uint32_t box_outer, bool swizzle128) {
+  CUtensorMap m;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = get_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr),
+                               dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                               swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    throw std::runtime_error("cuTensorMapEncodeTiled failed with code " + std::to_string((int)r));
+  return m;
+}
+
+template <int BN, int STAGES, int EPI>
+static void launch_impl(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
+                        int grid, cudaStream_t stream) {
+  constexpr int smem = STAGES * (kATileBytes + BN * kBK * 2) + 1024 + 256;
+  auto kern = gemm_bf16_kernel<BN, STAGES, EPI>;
+  static bool configured = false;  // one attribute call per instantiation
+  if (!configured) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    configured = true;
+  }
+  kern<<<grid, 192, smem, stream>>>(ta, tb, p);
+}
+
+int num_sms_cached() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+void gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
+  if (a.K % 8 != 0) throw std::invalid_argument("gemm: K must be a multiple of 8");
+  if (a.lda % 8 != 0 || a.ldb % 8 != 0)
+    throw std::invalid_argument("gemm: row pitches must be multiples of 8 elements");
+  const int bn = a.bn;
+  const CUtensorMap ta = make_tmap_bf16_2d(a.A, a.K, a.M, a.lda, kBK, kBM, true);
+  const CUtensorMap tb = make_tmap_bf16_2d(a.B, a.K, a.N, a.ldb, kBK, bn, true);
+  GemmParams p;
+  p.M = a.M;
+  p.N = a.N;
+  p.K = a.K;
+  p.num_m_blocks = (a.M + kBM - 1) / kBM;
+  p.num_n_blocks = (a.N + bn - 1) / bn;
+  if (a.epi == EPI_SILU_BF16) p.num_n_blocks = (a.N + bn - 1) / bn;  // N = 2 * I (interleaved)
+  p.num_k_blocks = (a.K + kBK - 1) / kBK;
+  int splits = a.splits < 1 ? 1 : a.splits;
+  if (splits > p.num_k_blocks) splits = p.num_k_blocks;
+  p.kb_per_split = (p.num_k_blocks + splits - 1) / splits;
+  p.splits = (p.num_k_blocks + p.kb_per_split - 1) / p.kb_per_split;  // no empty split
+  if (p.splits > 1 && (a.epi != EPI_F32_RED && a.epi != EPI_F32_RED_T))
+    throw std::invalid_argument("gemm: split-K requires an fp32 reduction epilogue");
+  p.group_m = a.group_m > 0 ? a.group_m : 16;
+  p.out = a.out;
+  p.ldo = a.ldo;
+  p.status = a.status;
+  const int tiles = p.num_m_blocks * p.num_n_blocks * p.splits;
+  int grid = num_sms_cached();
+  if (a.max_ctas > 0 && a.max_ctas < grid) grid = a.max_ctas;
+  if (tiles < grid) grid = tiles;
+
+#define B200_GEMM_CASE(BN_, ST_, EPI_)                                    \
+  if (bn == BN_ && a.epi == EPI_) {                                       \
+    launch_impl<BN_, ST_, EPI_>(ta, tb, p, grid, stream);                 \
+    return;                                                               \
+  }
+  B200_GEMM_CASE(256, 4, EPI_BF16)
+  B200_GEMM_CASE(128, 6, EPI_BF16)
+  B200_GEMM_CASE(256, 4, EPI_SILU_BF16)
+  B200_GEMM_CASE(128, 6, EPI_F32_RED)
+  B200_GEMM_CASE(256, 4, EPI_F32_RED)
+  B200_GEMM_CASE(16, 8, EPI_BF16_T)
+  B200_GEMM_CASE(32, 8, EPI_BF16_T)
+  B200_GEMM_CASE(64, 8, EPI_BF16_T)
+  B200_GEMM_CASE(128, 6, EPI_BF16_T)
+  B200_GEMM_CASE(16, 8, EPI_F32_RED_T)
+  B200_GEMM_CASE(32, 8, EPI_F32_RED_T)
+  B200_GEMM_CASE(64, 8, EPI_F32_RED_T)
+  B200_GEMM_CASE(128, 6, EPI_F32_RED_T)
+#undef B200_GEMM_CASE
+  throw std::invalid_argument("gemm: unsupported (bn, epilogue) combination: bn=" +
+                              std::to_string(bn) + " epi=" + std::to_string(a.epi));
+}
+
+}  // namespace b200

@@ -1,0 +1,62 @@
+// Host interface of the fused memory-bound kernels (norm_rope.cu, sampling.cu).
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace b200 {
+
+void add_rmsnorm_launch(void* x, bool x_is_f32, long long x_stride, __nv_bfloat16* residual,
+                        long long r_stride, const __nv_bfloat16* w, __nv_bfloat16* out,
+                        long long o_stride, int rows, int H, float eps, bool clear_x,
+                        cudaStream_t stream);
+
+struct RopeKvParams {
+  const int* positions;        // [T]
+  const long long* slot_mapping;  // [T] or null (no cache write)
+  const float* cos_sin;        // [max_pos, rot_dim]: cos in [0, rot/2), sin in [rot/2, rot)
+  long long qkv_stride;        // row stride of the qkv input (elements)
+  __nv_bfloat16* q_out;
+  long long q_out_stride;
+  __nv_bfloat16* k_cache;      // [num_blocks, Hkv, block_size, D]
+  __nv_bfloat16* v_cache;
+  long long kv_block_stride;
+  const __nv_bfloat16* q_norm_w;  // [D] or null
+  const __nv_bfloat16* k_norm_w;  // [D] or null
+  float eps;
+  int Hq, Hkv, head_dim, rot_dim, block_size;
+  bool neox;
+  bool clear_input;
+};
+void rope_kv_write_launch(const RopeKvParams& p, void* qkv, bool qkv_is_f32, int T,
+                          cudaStream_t stream);
+
+void silu_mul_launch(void* in, bool in_is_f32, long long in_stride, __nv_bfloat16* out,
+                     long long out_stride, int T, int I, int blk, bool clear_input, int act,
+                     float limit, float alpha, cudaStream_t stream);
+
+void embedding_launch(const int* ids, const __nv_bfloat16* table, __nv_bfloat16* out, int T,
+                      int H, int vocab_start, int vocab_end, cudaStream_t stream);
+
+struct SampleParams {
+  const void* logits;          // [B, V] (bf16 or fp32)
+  bool logits_f32;
+  long long logits_stride;
+  int B, V;
+  const float* temperature;    // [B]; <= 0 means greedy
+  const int* top_k;            // [B]; <= 0 or >= V disables
+  const float* top_p;          // [B]; >= 1 disables
+  const float* min_p;          // [B]; <= 0 disables (may be null)
+  const uint64_t* seeds;       // [B] per-row seeds
+  const int* offsets;          // [B] per-row step counters (RNG offset)
+  int* out_tokens;             // [B]
+  float* out_logprob;          // [B] log-probability of the sampled token (may be null)
+  int vocab_offset;            // added to the sampled index (vocab shard start)
+  float* out_max;              // [B] optional: row max of the processed logits (sharded merge)
+};
+void sample_launch(const SampleParams& p, cudaStream_t stream);
+
+void argmax_launch(const void* logits, bool f32, long long stride, int B, int V, int* out_idx,
+                   float* out_val, int vocab_offset, cudaStream_t stream);
+
+}  // namespace b200

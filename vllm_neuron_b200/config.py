@@ -1,0 +1,227 @@
+"""Model and framework configuration.
+
+``ModelArchConfig`` normalises a HuggingFace ``config.json`` (Llama-3, Qwen3, GPT-OSS, Qwen3
+hybrid) into the fields the models use.  ``B200Config`` parses the plugin options that
+users pass as ``additional_config={"neuron_config": {...}}`` (the reference's key names are
+accepted verbatim, ``"b200_config"`` is an alias) -- reference:
+vllm_neuron/model/neuron_config.py:8-485.
+"""
+from __future__ import annotations
+
+import dataclasses
+import json
+import os
+from dataclasses import dataclass, field
+from typing import Any
+
+
+@dataclass
+class ModelArchConfig:
+    model_type: str = "llama"
+    architectures: tuple = ("LlamaForCausalLM",)
+    hidden_size: int = 4096
+    num_layers: int = 32
+    num_heads: int = 32
+    num_kv_heads: int = 8
+    head_dim: int = 128
+    intermediate_size: int = 14336
+    vocab_size: int = 128256
+    rms_norm_eps: float = 1e-5
+    rope_theta: float = 500000.0
+    rope_scaling: dict | None = None
+    partial_rotary_factor: float = 1.0
+    max_position_embeddings: int = 8192
+    tie_word_embeddings: bool = False
+    qk_norm: bool = False
+    attention_bias: bool = False
+    # MoE
+    num_experts: int = 0
+    num_experts_per_tok: int = 0
+    moe_intermediate_size: int = 0
+    shared_expert_intermediate_size: int = 0
+    norm_topk_prob: bool = True
+    # sliding window / sinks (GPT-OSS)
+    sliding_window: int = 0
+    layer_types: tuple = ()
+    attention_sinks: bool = False
+    swiglu_limit: float = 7.0
+    swiglu_alpha: float = 1.702
+    # hybrid linear attention (Qwen3-Next style)
+    linear_num_key_heads: int = 0
+    linear_num_value_heads: int = 0
+    linear_key_head_dim: int = 0
+    linear_value_head_dim: int = 0
+    linear_conv_kernel_dim: int = 0
+    full_attention_interval: int = 0
+    attn_output_gate: bool = False
+    # quantization
+    quant_method: str | None = None
+    weight_block_size: tuple | None = None
+    raw: dict = field(default_factory=dict, repr=False)
+
+    @classmethod
+    def from_hf(cls, cfg: dict) -> "ModelArchConfig":
+        if hasattr(cfg, "to_dict"):
+            cfg = cfg.to_dict()
+        cfg = dict(cfg)
+        if "text_config" in cfg and cfg.get("model_type", "").endswith("_vl"):
+            text = dict(cfg["text_config"])
+            text.setdefault("architectures", cfg.get("architectures"))
+            cfg = {**cfg, **text}
+        H = cfg.get("hidden_size", 4096)
+        nh = cfg.get("num_attention_heads", 32)
+        head_dim = cfg.get("head_dim") or H // nh
+        qcfg = cfg.get("quantization_config") or {}
+        c = cls(
+            model_type=cfg.get("model_type", "llama"),
+            architectures=tuple(cfg.get("architectures") or ("LlamaForCausalLM",)),
+            hidden_size=H,
+            num_layers=cfg.get("num_hidden_layers", 32),
+            num_heads=nh,
+            num_kv_heads=cfg.get("num_key_value_heads", nh),
+            head_dim=head_dim,
+            intermediate_size=cfg.get("intermediate_size", 4 * H),
+            vocab_size=cfg.get("vocab_size", 32000),
+            rms_norm_eps=cfg.get("rms_norm_eps", 1e-5),
+            rope_theta=cfg.get("rope_theta", 10000.0),
+            rope_scaling=cfg.get("rope_scaling"),
+            partial_rotary_factor=cfg.get("partial_rotary_factor", 1.0),
+            max_position_embeddings=cfg.get("max_position_embeddings", 8192),
+            tie_word_embeddings=cfg.get("tie_word_embeddings", False),
+            qk_norm=cfg.get("model_type", "") in ("qwen3", "qwen3_moe", "qwen3_next", "qwen3_vl"),
+            attention_bias=cfg.get("attention_bias", False),
+            num_experts=cfg.get("num_local_experts", cfg.get("num_experts", 0)) or 0,
+            num_experts_per_tok=cfg.get("num_experts_per_tok", cfg.get("experts_per_token", 0)) or 0,
+            moe_intermediate_size=cfg.get("moe_intermediate_size", 0) or 0,
+            shared_expert_intermediate_size=cfg.get("shared_expert_intermediate_size", 0) or 0,
+            norm_topk_prob=cfg.get("norm_topk_prob", True),
+            sliding_window=cfg.get("sliding_window") or 0,
+            layer_types=tuple(cfg.get("layer_types") or ()),
+            attention_sinks=cfg.get("model_type") == "gpt_oss",
+            swiglu_limit=cfg.get("swiglu_limit", 7.0),
+            linear_num_key_heads=cfg.get("linear_num_key_heads", 0) or 0,
+            linear_num_value_heads=cfg.get("linear_num_value_heads", 0) or 0,
+            linear_key_head_dim=cfg.get("linear_key_head_dim", 0) or 0,
+            linear_value_head_dim=cfg.get("linear_value_head_dim", 0) or 0,
+            linear_conv_kernel_dim=cfg.get("linear_conv_kernel_dim", 0) or 0,
+            full_attention_interval=cfg.get("full_attention_interval", 0) or 0,
+            attn_output_gate=cfg.get("attn_output_gate", cfg.get("model_type") == "qwen3_next"),
+            quant_method=qcfg.get("quant_method"),
+            weight_block_size=tuple(qcfg["weight_block_size"]) if qcfg.get("weight_block_size") else None,
+            raw=cfg,
+        )
+        if c.model_type == "gpt_oss":
+            c.intermediate_size = cfg.get("intermediate_size", c.intermediate_size)
+            c.attention_bias = True
+        return c
+
+    @classmethod
+    def from_path(cls, path: str) -> "ModelArchConfig":
+        with open(os.path.join(path, "config.json")) as f:
+            return cls.from_hf(json.load(f))
+
+    @property
+    def rot_dim(self) -> int:
+        return int(self.head_dim * self.partial_rotary_factor)
+
+    def layer_is_sliding(self, i: int) -> bool:
+        if self.layer_types:
+            return self.layer_types[i] == "sliding_attention"
+        return False
+
+    def layer_is_linear(self, i: int) -> bool:
+        if self.layer_types:
+            return self.layer_types[i] == "linear_attention"
+        if self.full_attention_interval:
+            return (i + 1) % self.full_attention_interval != 0
+        return False
+
+
+# -------------------------------------------------------------------------------------------
+# Framework options (reference NeuronConfig keys accepted verbatim)
+# -------------------------------------------------------------------------------------------
+@dataclass
+class OnDeviceSamplingConfig:
+    """Reference: vllm_neuron/model/neuron_config.py:8-37 (enabled by default)."""
+
+    enabled: bool = True
+    do_sample: bool = True
+    global_topk: int = 256
+    deterministic: bool = False
+    dynamic: bool = True
+
+
+@dataclass
+class B200Config:
+    """Options under ``additional_config["neuron_config"]`` (or ``"b200_config"``)."""
+
+    ep_degree: int | None = None
+    attention_dp_size: int = 1
+    embedding_dp_size: int = 1
+    lm_head_dp_size: int = 1
+    mlp_dp_size: int = 1
+    on_device_sampling_config: OnDeviceSamplingConfig = field(default_factory=OnDeviceSamplingConfig)
+    max_logprobs: int = 0
+    tensor_capture: dict | None = None
+    tensor_replacement: dict | None = None
+    kv_segment_size_buckets: list | None = None
+    debug_logits_dir: str | None = None
+    quantization: str | None = None
+    all2all_backend: str | None = None
+    modules_to_not_convert: list | None = None
+    num_batched_tokens_buckets: list | None = None
+    num_seqs_buckets: list | None = None
+    decode_context_length_buckets: list | None = None
+    enable_structured_outputs: bool = True
+    fp8_packed_kv: bool = False
+    # B200-specific knobs
+    cuda_graphs: bool = True
+    fused_comm: bool = True           # fused GEMM+collective kernels (else NCCL baseline)
+    use_cublas_baseline: bool = False  # library GEMMs instead of the tcgen05 kernels
+    extra: dict = field(default_factory=dict)
+
+    @classmethod
+    def from_dict(cls, d: dict | None) -> "B200Config":
+        d = dict(d or {})
+        known = {f.name for f in dataclasses.fields(cls)}
+        kw: dict[str, Any] = {}
+        extra = {}
+        for k, v in d.items():
+            if k == "on_device_sampling_config":
+                if v is None:
+                    kw[k] = OnDeviceSamplingConfig(enabled=False)
+                elif isinstance(v, dict):
+                    kw[k] = OnDeviceSamplingConfig(**v)
+                else:
+                    kw[k] = v
+            elif k in known:
+                kw[k] = v
+            else:
+                extra[k] = v
+        c = cls(**kw)
+        c.extra = extra
+        c.validate()
+        return c
+
+    @classmethod
+    def from_additional_config(cls, additional: dict | None) -> "B200Config":
+        additional = additional or {}
+        d = additional.get("b200_config") or additional.get("neuron_config") or {}
+        return cls.from_dict(d)
+
+    def validate(self):
+        for name in ("attention_dp_size", "embedding_dp_size", "lm_head_dp_size", "mlp_dp_size"):
+            v = getattr(self, name)
+            if not isinstance(v, int) or v < 1:
+                raise ValueError(f"{name} must be a positive integer, got {v!r}")
+        for name in ("num_batched_tokens_buckets", "num_seqs_buckets", "decode_context_length_buckets",
+                     "kv_segment_size_buckets"):
+            v = getattr(self, name)
+            if v is not None:
+                if not all(isinstance(x, int) and x > 0 for x in v):
+                    raise ValueError(f"{name} must be a list of positive integers")
+                setattr(self, name, sorted(set(v)))
+        if self.all2all_backend not in (None, "neuron", "nvlink", "nccl"):
+            raise ValueError(f"unknown all2all_backend {self.all2all_backend!r}")
+        if self.quantization not in (None, "fp8", "mxfp4", "mxfp8", "modelopt_fp8"):
+            raise ValueError(f"unknown quantization {self.quantization!r}")

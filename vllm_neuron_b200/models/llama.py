@@ -1,0 +1,258 @@
+"""Llama-3 / Qwen3 dense decoder on the sm_100a kernels, tensor parallel over a GroupComm.
+
+Per layer (TP world W, local heads Hq/W and Hkv/W, local FFN I/W):
+
+  prefill / mixed batches (tokens > 128):
+    qkv  = x @ Wqkv^T                         tcgen05 GEMM, bf16 out
+    q, k/v -> cache                           rope_kv_write (RoPE, optional QK-norm)
+    a    = paged_attention(q, cache)
+    o    = a @ Wo^T  -> all-reduce (W > 1)    row-parallel
+    x    = rmsnorm(residual += o)
+    act  = silu(x @ Wg^T) * (x @ Wu^T)        one GEMM with the SwiGLU epilogue
+    d    = act @ Wd^T -> all-reduce
+    x    = rmsnorm(residual += d)             (the next layer's input norm)
+
+  decode batches (tokens <= 128): the same with swapped-operand split-K GEMMs that
+  accumulate in fp32 buffers; the consumer kernels read and clear those buffers, and the
+  all-reduce (W > 1) runs on the fp32 buffer.
+
+Weights: ``qkv [(Hq + 2 Hkv) D / W, H]``, ``o [H, Hq D / W]``, ``gate_up`` rows interleaved
+in 128-row blocks ``[2 I / W, H]``, ``down [H, I / W]``, vocab-sharded embedding and LM head.
+
+Reference: vllm_neuron/model/llama3/model.py (LlamaAttention :333-991, LlamaMLP
+:1017-1115, LlamaModel.forward :1424, LlamaForCausalLM.forward :1610) and
+vllm_neuron/model/qwen3/model.py (QK-norm).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from .. import ops
+from ..config import ModelArchConfig
+from ..ops import linear as L
+from ..parallel.comm import SINGLE, GroupComm
+
+
+@dataclass
+class ForwardBatch:
+    """Device-side inputs of one forward pass (built by the model runner)."""
+
+    input_ids: torch.Tensor      # [T] int32
+    positions: torch.Tensor      # [T] int32
+    slot_mapping: torch.Tensor   # [T] int64 (-1 = do not write)
+    block_tables: torch.Tensor   # [B, max_blocks] int32
+    seq_lens: torch.Tensor       # [B] int32
+    q_start: torch.Tensor        # [B + 1] int32
+    work: torch.Tensor           # [W, 2] int32 attention work items
+    logits_indices: torch.Tensor  # [S] int64 rows whose logits are needed
+    decode: bool
+    num_splits: int
+    num_tokens: int
+
+
+def _shard(n: int, world: int, rank: int) -> tuple[int, int]:
+    assert n % world == 0, f"{n} not divisible by TP={world}"
+    per = n // world
+    return rank * per, per
+
+
+class LlamaForCausalLM(torch.nn.Module):
+    """Dense Llama-3 / Qwen3 decoder (the ``LlamaForCausalLM`` / ``Qwen3ForCausalLM`` archs)."""
+
+    def __init__(self, cfg: ModelArchConfig, tp: GroupComm = SINGLE, device="cuda",
+                 dtype=torch.bfloat16, max_tokens: int = 8192, max_decode_tokens: int = 128,
+                 max_seqs: int = 256, block_size: int = 16):
+        super().__init__()
+        self.cfg = cfg
+        self.tp = tp
+        self.device = torch.device(device)
+        self.dtype = dtype
+        W = tp.world
+        self.Hq = cfg.num_heads // W
+        # KV heads are replicated when TP exceeds their count.
+        self.kv_rep = max(1, W // cfg.num_kv_heads)
+        self.Hkv = max(1, cfg.num_kv_heads // W)
+        self.D = cfg.head_dim
+        self.H = cfg.hidden_size
+        self.I = cfg.intermediate_size // W
+        self.V = cfg.vocab_size
+        self.V_local = math.ceil(cfg.vocab_size / W)
+        self.vocab_start = tp.rank * self.V_local
+        self.eps = cfg.rms_norm_eps
+        self.scale = 1.0 / math.sqrt(self.D)
+        self.silu_blk = L.SILU_BLOCK if self.I % L.SILU_BLOCK == 0 else 0
+        self.block_size = block_size
+        self.max_decode_tokens = max_decode_tokens
+        self.max_tokens = max_tokens
+        qkv_out = (self.Hq + 2 * self.Hkv) * self.D
+        self.qkv_out = qkv_out
+        p = lambda *s: torch.nn.Parameter(torch.empty(*s, dtype=dtype, device=self.device), requires_grad=False)
+        self.embed = p(self.V_local, self.H)
+        self.layers = torch.nn.ModuleList()
+        for _ in range(cfg.num_layers):
+            m = torch.nn.Module()
+            m.input_norm = p(self.H)
+            m.post_norm = p(self.H)
+            m.qkv = p(qkv_out, self.H)
+            m.qkv_bias = p(qkv_out) if cfg.attention_bias else None
+            m.o = p(self.H, self.Hq * self.D)
+            m.gate_up = p(2 * self.I, self.H)
+            m.down = p(self.H, self.I)
+            if cfg.qk_norm:
+                m.q_norm = p(self.D)
+                m.k_norm = p(self.D)
+            else:
+                m.q_norm = m.k_norm = None
+            self.layers.append(m)
+        self.final_norm = p(self.H)
+        self.lm_head = self.embed if cfg.tie_word_embeddings else p(self.V_local, self.H)
+        self.cos_sin = ops.cos_sin_table(cfg.max_position_embeddings, cfg.rot_dim, cfg.rope_theta,
+                                         cfg.rope_scaling, device=self.device)
+        self.kv_caches: list[tuple[torch.Tensor, torch.Tensor]] = []
+        self._alloc_workspace(max_tokens, max_decode_tokens, max_seqs)
+
+    # ---------------------------------------------------------------- init / weights
+    def _alloc_workspace(self, max_tokens, max_dec, max_seqs):
+        d, bf = self.device, self.dtype
+        self.ws_residual = torch.zeros(max_tokens, self.H, dtype=bf, device=d)
+        self.ws_x = torch.zeros(max_tokens, self.H, dtype=bf, device=d)
+        self.ws_qkv = torch.zeros(max_tokens, self.qkv_out, dtype=bf, device=d)
+        self.ws_q = torch.zeros(max_tokens, self.Hq * self.D, dtype=bf, device=d)
+        self.ws_attn = torch.zeros(max_tokens, self.Hq * self.D, dtype=bf, device=d)
+        self.ws_h = torch.zeros(max_tokens, self.H, dtype=bf, device=d)
+        self.ws_act = torch.zeros(max_tokens, self.I, dtype=bf, device=d)
+        # fp32 accumulation buffers of the decode path (kept zero between uses)
+        self.acc_qkv = torch.zeros(max_dec, self.qkv_out, dtype=torch.float32, device=d)
+        self.acc_h = torch.zeros(max_dec, self.H, dtype=torch.float32, device=d)
+        self.acc_gu = torch.zeros(max_dec, 2 * self.I, dtype=torch.float32, device=d)
+        self.ws_logits_x = torch.zeros(max_seqs, self.H, dtype=bf, device=d)
+        self.ws_logits = torch.zeros(max_seqs, self.V_local, dtype=bf, device=d)
+        self.attn_splits_max = 16
+        self.ws_part_o = torch.zeros(self.attn_splits_max * max_dec * self.Hq * self.D,
+                                     dtype=torch.float32, device=d)
+        self.ws_part_lse = torch.zeros(self.attn_splits_max * max_dec * self.Hq,
+                                       dtype=torch.float32, device=d)
+
+    @torch.no_grad()
+    def init_random(self, seed: int = 0, std: float = 0.02):
+        """Random-init N(0, std) weights (norms = 1).  Each TP rank draws its own shard."""
+        g = torch.Generator(device=self.device)
+        g.manual_seed(seed * 1000 + self.tp.rank)
+        for name, prm in self.named_parameters():
+            if prm is None:
+                continue
+            if "norm" in name:
+                prm.fill_(1.0)
+            elif name.endswith("bias"):
+                prm.zero_()
+            else:
+                prm.normal_(0.0, std, generator=g)
+
+    def bind_kv_cache(self, kv_caches: list[tuple[torch.Tensor, torch.Tensor]]):
+        assert len(kv_caches) == self.cfg.num_layers
+        self.kv_caches = kv_caches
+
+    def kv_cache_shape(self, num_blocks: int) -> tuple[int, ...]:
+        return (num_blocks, self.Hkv, self.block_size, self.D)
+
+    def kv_bytes_per_block(self) -> int:
+        return 2 * self.cfg.num_layers * self.Hkv * self.block_size * self.D * 2
+
+    # ---------------------------------------------------------------- forward
+    @torch.no_grad()
+    def forward(self, b: ForwardBatch) -> torch.Tensor:
+        """Returns logits ``[len(logits_indices), V]`` (bf16, full vocab on every rank)."""
+        T = b.num_tokens
+        small = T <= self.max_decode_tokens
+        tp = self.tp
+        res = self.ws_residual[:T]
+        x = self.ws_x[:T]
+        ops.embedding(b.input_ids, self.embed, self.vocab_start, self.vocab_start + self.V_local, out=res)
+        tp.all_reduce_(res)
+        ops.rmsnorm(res, self.layers[0].input_norm, self.eps, out=x)
+        nL = len(self.layers)
+        for i, ly in enumerate(self.layers):
+            k_cache, v_cache = self.kv_caches[i]
+            q = self.ws_q[:T]
+            # ---- attention
+            if small:
+                acc = self.acc_qkv[:T]
+                L.gemm_accumulate(x, ly.qkv, acc)
+                if ly.qkv_bias is not None:
+                    acc.add_(ly.qkv_bias.float())
+                ops.rope_kv_write(acc, b.positions, self.cos_sin, self.Hq, self.Hkv, self.D, q,
+                                  k_cache, v_cache, b.slot_mapping, ly.q_norm, ly.k_norm, self.eps,
+                                  rot_dim=self.cfg.rot_dim, clear_input=True)
+            else:
+                qkv = L.gemm_out(x, ly.qkv, out=self.ws_qkv[:T])
+                if ly.qkv_bias is not None:
+                    qkv.add_(ly.qkv_bias)
+                ops.rope_kv_write(qkv, b.positions, self.cos_sin, self.Hq, self.Hkv, self.D, q,
+                                  k_cache, v_cache, b.slot_mapping, ly.q_norm, ly.k_norm, self.eps,
+                                  rot_dim=self.cfg.rot_dim)
+            attn = self.ws_attn[:T]
+            self._attention(q, attn, k_cache, v_cache, b)
+            nxt_norm = ly.post_norm
+            if small:
+                acc = self.acc_h[:T]
+                L.gemm_accumulate(attn, ly.o, acc)
+                tp.all_reduce_(acc)
+                ops.add_rmsnorm(acc, res, nxt_norm, self.eps, out=x, clear_x=True)
+            else:
+                h = L.gemm_out(attn, ly.o, out=self.ws_h[:T])
+                tp.all_reduce_(h)
+                ops.add_rmsnorm(h, res, nxt_norm, self.eps, out=x)
+            # ---- MLP
+            nxt_norm = self.layers[i + 1].input_norm if i + 1 < nL else self.final_norm
+            if small:
+                acc = self.acc_gu[:T]
+                L.gemm_accumulate(x, ly.gate_up, acc)
+                act = ops.silu_mul(acc, out=self.ws_act[:T], blk=self.silu_blk, clear_input=True)
+                acc = self.acc_h[:T]
+                L.gemm_accumulate(act, ly.down, acc)
+                tp.all_reduce_(acc)
+                ops.add_rmsnorm(acc, res, nxt_norm, self.eps, out=x, clear_x=True)
+            else:
+                if self.silu_blk:
+                    act = L.gemm_silu(x, ly.gate_up, out=self.ws_act[:T])
+                else:
+                    gu = L.gemm_out(x, ly.gate_up)
+                    act = ops.silu_mul(gu, out=self.ws_act[:T])
+                h = L.gemm_out(act, ly.down, out=self.ws_h[:T])
+                tp.all_reduce_(h)
+                ops.add_rmsnorm(h, res, nxt_norm, self.eps, out=x)
+        return self.compute_logits(x, b.logits_indices)
+
+    def _attention(self, q, attn, k_cache, v_cache, b: ForwardBatch, window: int = 0, sinks=None):
+        T = b.num_tokens
+        ns = b.num_splits
+        part_o = part_l = None
+        if ns > 1:
+            part_o = self.ws_part_o[: ns * T * self.Hq * self.D].view(ns, T, self.Hq, self.D)
+            part_l = self.ws_part_lse[: ns * T * self.Hq].view(ns, T, self.Hq)
+        ops.paged_attention(q.view(T, self.Hq, self.D), k_cache, v_cache, b.block_tables, b.seq_lens,
+                            b.q_start, b.work, b.decode, ns, self.scale, window=window, sinks=sinks,
+                            out=attn.view(T, self.Hq, self.D), part_o=part_o, part_lse=part_l)
+
+    def compute_logits(self, x: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:
+        S = idx.shape[0]
+        xs = self.ws_logits_x[:S]
+        torch.index_select(x, 0, idx, out=xs)
+        logits = self.ws_logits[:S]
+        if S <= L.SKINNY_MAX and x.is_cuda:
+            L.gemm_skinny_bf16(xs, self.lm_head, out=logits)
+        else:
+            L.gemm_out(xs, self.lm_head, out=logits)
+        if self.tp.world > 1:
+            logits = self.tp.all_gather(logits, dim=1)
+        return logits[:, : self.V]
+
+    # ---------------------------------------------------------------- HF weight loading
+    def load_hf_state_dict(self, get_tensor, names: set[str]):
+        """Load from HF tensor names.  ``get_tensor(name)`` returns a CPU tensor."""
+        from ..utils.weight_loader import load_dense_decoder
+
+        load_dense_decoder(self, get_tensor, names)

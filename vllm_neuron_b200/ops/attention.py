@@ -1,0 +1,132 @@
+"""Paged GQA attention (csrc/attn/paged_attention.cu) and its fp32 torch oracle.
+
+KV cache per layer: ``k_cache, v_cache`` of shape ``[num_blocks, num_kv_heads, block_size,
+head_dim]``.  Batch metadata (built on the host once per step, shared by all layers):
+
+* ``q_start [B+1]`` cumulative query lengths, ``seq_lens [B]`` total KV length per sequence
+  (cached tokens + tokens of this step), ``block_tables [B, max_blocks]``;
+* ``work [W, 2]`` (sequence, first packed row) for the CTAs;
+* ``num_splits``: split-KV factor (decode only).
+
+Reference semantics: ``flash_attention`` / ``segmented_attention`` / ``attention_decode``
+(vllm_neuron/functional/attention/attention_cte.py:189, attention_segmented_cte.py:657,
+attention_decode.py:1266): causal, sliding window, learned sinks, paged prior KV.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from ._ext import ext
+
+PREFILL_ROWS = 64
+DECODE_ROWS = 16
+KV_TILE = 64
+
+
+@dataclass
+class AttnWork:
+    """Host-side work decomposition for one batch (independent of the layer)."""
+
+    work: np.ndarray  # [W, 2] int32
+    decode: bool
+    num_splits: int
+
+
+def build_work(q_lens: np.ndarray, seq_lens: np.ndarray, group: int, num_kv_heads: int,
+               num_sms: int = 148, max_splits: int = 16) -> AttnWork:
+    """Split the batch into CTA work items.
+
+    Decode mode is used when every sequence has at most ``DECODE_ROWS`` packed rows
+    (q_len * group); it then also picks a split-KV factor so the grid covers the SMs.
+    """
+    q_lens = np.asarray(q_lens, dtype=np.int64)
+    rows = q_lens * group
+    decode = bool(len(rows) > 0 and rows.max() <= DECODE_ROWS)
+    if decode:
+        work = np.stack([np.arange(len(rows)), np.zeros(len(rows), dtype=np.int64)], 1)
+        ctas = len(rows) * num_kv_heads
+        max_tiles = int(math.ceil(int(np.max(seq_lens)) / KV_TILE)) if len(rows) else 1
+        splits = 1
+        while ctas * splits < 2 * num_sms and splits * 2 <= min(max_splits, max(1, max_tiles // 2)):
+            splits *= 2
+        return AttnWork(work.astype(np.int32), True, splits)
+    seqs, starts = [], []
+    for b, r in enumerate(rows):
+        n = int(math.ceil(r / PREFILL_ROWS))
+        # Longest-first ordering is applied by sorting work items by remaining KV length.
+        for t in range(n):
+            seqs.append(b)
+            starts.append(t * PREFILL_ROWS)
+    work = np.stack([np.asarray(seqs, dtype=np.int64), np.asarray(starts, dtype=np.int64)], 1) \
+        if seqs else np.zeros((0, 2), dtype=np.int64)
+    if len(work):
+        # Heaviest tiles first: the later rows of the longest sequences see the most KV.
+        ctx = np.asarray(seq_lens, dtype=np.int64)[work[:, 0]] - q_lens[work[:, 0]] + work[:, 1] // group
+        work = work[np.argsort(-ctx, kind="stable")]
+    return AttnWork(work.astype(np.int32), False, 1)
+
+
+def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                    block_tables: torch.Tensor, seq_lens: torch.Tensor, q_start: torch.Tensor,
+                    work: torch.Tensor, decode: bool, num_splits: int, scale: float,
+                    window: int = 0, sinks: torch.Tensor | None = None,
+                    out: torch.Tensor | None = None, part_o: torch.Tensor | None = None,
+                    part_lse: torch.Tensor | None = None) -> torch.Tensor:
+    """Attention of ``q [T, Hq, D]`` over the paged cache; returns ``out [T, Hq, D]``."""
+    if out is None:
+        out = torch.empty_like(q)
+    if not q.is_cuda:
+        out.copy_(paged_attention_ref(q, k_cache, v_cache, block_tables, seq_lens, q_start,
+                                      scale, window, sinks).to(out.dtype))
+        return out
+    T, Hq, D = q.shape
+    if num_splits > 1 and (part_o is None or part_lse is None):
+        part_o = torch.empty((num_splits, T, Hq, D), dtype=torch.float32, device=q.device)
+        part_lse = torch.empty((num_splits, T, Hq), dtype=torch.float32, device=q.device)
+    ext().paged_attention(q, k_cache, v_cache, block_tables, seq_lens, q_start, work, out,
+                          part_o, part_lse, sinks, num_splits, k_cache.shape[1], window, scale,
+                          decode)
+    return out
+
+
+def paged_attention_ref(q, k_cache, v_cache, block_tables, seq_lens, q_start, scale,
+                        window=0, sinks=None) -> torch.Tensor:
+    """fp32 oracle: gathers each sequence's KV from its blocks and runs masked softmax."""
+    T, Hq, D = q.shape
+    Hkv, bs = k_cache.shape[1], k_cache.shape[2]
+    G = Hq // Hkv
+    out = torch.zeros((T, Hq, D), dtype=torch.float32, device=q.device)
+    qs = q_start.tolist()
+    sl = seq_lens.tolist()
+    bt = block_tables.cpu()
+    for b in range(len(sl)):
+        q0, q1, L = qs[b], qs[b + 1], sl[b]
+        if q1 == q0:
+            continue
+        nblk = (L + bs - 1) // bs
+        blocks = bt[b, :nblk].to(k_cache.device).long()
+        k = k_cache[blocks].float().permute(1, 0, 2, 3).reshape(Hkv, nblk * bs, D)[:, :L]
+        v = v_cache[blocks].float().permute(1, 0, 2, 3).reshape(Hkv, nblk * bs, D)[:, :L]
+        k = k.repeat_interleave(G, dim=0)
+        v = v.repeat_interleave(G, dim=0)
+        qq = q[q0:q1].float().permute(1, 0, 2)  # [Hq, n, D]
+        s = torch.einsum("hnd,hld->hnl", qq, k) * scale
+        n = q1 - q0
+        pos = torch.arange(L - n, L, device=q.device)[:, None]
+        j = torch.arange(L, device=q.device)[None, :]
+        mask = j <= pos
+        if window and window > 0:
+            mask = mask & (j > pos - window)
+        s = s.masked_fill(~mask[None], float("-inf"))
+        if sinks is not None:
+            sink = sinks.float().view(Hq, 1, 1).expand(Hq, n, 1)
+            s = torch.cat([s, sink], dim=-1)
+            p = torch.softmax(s, dim=-1)[..., :-1]
+        else:
+            p = torch.softmax(s, dim=-1)
+        out[q0:q1] = torch.einsum("hnl,hld->hnd", p, v).permute(1, 0, 2)
+    return out

@@ -1,0 +1,161 @@
+"""Dense projections on the tcgen05 GEMM (csrc/gemm/gemm_sm100.cu).
+
+Weights are stored ``[out_features, in_features]`` (K-contiguous, as checkpoints store them),
+activations ``[tokens, in_features]``.  Two regimes:
+
+* ``tokens > SKINNY_MAX`` (prefill / mixed batches): ``out = x @ w^T`` with 128 x BN tiles,
+  BN picked to minimise the persistent-wave makespan over the SMs.
+* ``tokens <= SKINNY_MAX`` (decode): operands are swapped so the weight rows fill the
+  128-row MMA dimension and the tokens become a narrow N tile (16..128).  The K loop is
+  split until the grid covers the SMs, and the partial sums are reduced in fp32 into an
+  accumulation buffer that the consumer kernel (add_rmsnorm / rope_kv_write / silu_mul)
+  reads and clears.
+
+Reference counterparts: ``ColumnParallelLinear`` / ``RowParallelLinear``
+(vllm_neuron/nn/cpl.py:27, nn/rpl.py:23) and the NKI projection kernels they feed
+(functional/attention/o_proj.py:124, functional/mlp.py:65).
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from ._ext import ext
+
+EPI_BF16 = 0
+EPI_BF16_T = 1
+EPI_F32_RED = 2
+EPI_F32_RED_T = 3
+EPI_SILU_BF16 = 4
+
+SKINNY_MAX = 128
+SILU_BLOCK = 128  # gate/up interleave block = BN/2 of the fused SwiGLU epilogue
+
+_NUM_SMS: dict[int, int] = {}
+
+
+def num_sms(device: torch.device) -> int:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if idx not in _NUM_SMS:
+        _NUM_SMS[idx] = torch.cuda.get_device_properties(idx).multi_processor_count
+    return _NUM_SMS[idx]
+
+
+def _pick_bn_wide(m: int, n: int, sms: int) -> int:
+    """Pick the N tile (128 or 256) that minimises waves * tile-time for a wide GEMM."""
+    best, best_cost = 256, float("inf")
+    mb = math.ceil(m / 128)
+    for bn, cost_per_tile in ((256, 2.0), (128, 1.08)):
+        tiles = mb * math.ceil(n / bn)
+        waves = math.ceil(tiles / sms)
+        cost = waves * cost_per_tile
+        if cost < best_cost - 1e-9:
+            best, best_cost = bn, cost
+    return best
+
+
+def skinny_bn(m: int) -> int:
+    for bn in (16, 32, 64, 128):
+        if m <= bn:
+            return bn
+    raise ValueError(m)
+
+
+def pick_splits(n_rows: int, k: int, sms: int) -> int:
+    """Split-K factor so that (row tiles x splits) covers the SMs, keeping >= 4 K-blocks."""
+    tiles = math.ceil(n_rows / 128)
+    kb = math.ceil(k / 64)
+    if tiles >= sms:
+        return 1
+    s = max(1, min(sms // tiles, kb // 4))
+    return s
+
+
+def gemm_out(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,
+             bn: int | None = None) -> torch.Tensor:
+    """``out[M, N] = x[M, K] @ w[N, K]^T`` in bf16 (wide regime, no split-K)."""
+    M, K = x.shape
+    N = w.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    if not x.is_cuda:
+        out.copy_((x.float() @ w.float().t()).to(out.dtype))
+        return out
+    if bn is None:
+        bn = _pick_bn_wide(M, N, num_sms(x.device))
+    ext().gemm(x, w, out, EPI_BF16, bn, 1, 0, 0)
+    return out
+
+
+def gemm_skinny_bf16(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Decode regime without split-K: swapped operands, transposed bf16 store."""
+    M, K = x.shape
+    N = w.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    if not x.is_cuda:
+        out.copy_((x.float() @ w.float().t()).to(out.dtype))
+        return out
+    ext().gemm(w, x, out, EPI_BF16_T, skinny_bn(M), 1, 0, 0)
+    return out
+
+
+def gemm_accumulate(x: torch.Tensor, w: torch.Tensor, acc: torch.Tensor,
+                    splits: int | None = None) -> torch.Tensor:
+    """``acc[M, N] += x @ w^T`` in fp32 (split-K; the consumer clears ``acc`` after use).
+
+    ``acc`` must be zero on entry (the fused consumers leave it zeroed).
+    """
+    M, K = x.shape
+    N = w.shape[0]
+    assert acc.dtype == torch.float32 and acc.shape[0] >= M and acc.shape[1] == N
+    if not x.is_cuda:
+        acc[:M].add_(x.float() @ w.float().t())
+        return acc
+    sms = num_sms(x.device)
+    if M <= SKINNY_MAX:
+        s = splits if splits is not None else pick_splits(N, K, sms)
+        ext().gemm(w, x, acc, EPI_F32_RED_T, skinny_bn(M), s, 0, 0)
+    else:
+        bn = 128
+        tiles = math.ceil(M / 128) * math.ceil(N / bn)
+        s = splits if splits is not None else (1 if tiles >= sms else max(1, min(sms // tiles, math.ceil(K / 64) // 4)))
+        ext().gemm(x, w, acc, EPI_F32_RED, bn, s, 0, 0)
+    return acc
+
+
+def gemm_silu(x: torch.Tensor, w_gu: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Fused ``silu(x @ g^T) * (x @ u^T)`` where ``w_gu`` interleaves gate/up rows in blocks of
+    ``SILU_BLOCK`` (see :func:`interleave_gate_up`)."""
+    M, K = x.shape
+    N2 = w_gu.shape[0]
+    if out is None:
+        out = torch.empty((M, N2 // 2), dtype=torch.bfloat16, device=x.device)
+    if not x.is_cuda:
+        y = x.float() @ w_gu.float().t()
+        out.copy_(silu_mul_ref(y, SILU_BLOCK).to(out.dtype))
+        return out
+    ext().gemm(x, w_gu, out, EPI_SILU_BF16, 2 * SILU_BLOCK, 1, 0, 0)
+    return out
+
+
+def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor, blk: int = SILU_BLOCK) -> torch.Tensor:
+    """Rows ``[g[0:blk], u[0:blk], g[blk:2blk], u[blk:2blk], ...]`` (requires I % blk == 0)."""
+    I, K = gate.shape
+    assert up.shape == gate.shape and I % blk == 0
+    return torch.stack([gate.view(I // blk, blk, K), up.view(I // blk, blk, K)], dim=1).reshape(2 * I, K)
+
+
+def silu_mul_ref(y: torch.Tensor, blk: int) -> torch.Tensor:
+    """fp32 reference of SwiGLU on a [T, 2I] tensor whose gate/up columns are interleaved in
+    blocks of ``blk`` (``blk == 0``: first half gate, second half up)."""
+    T, I2 = y.shape
+    I = I2 // 2
+    if blk > 0:
+        v = y.view(T, I // blk, 2, blk)
+        g, u = v[:, :, 0, :].reshape(T, I), v[:, :, 1, :].reshape(T, I)
+    else:
+        g, u = y[:, :I], y[:, I:]
+    g = g.float()
+    return torch.nn.functional.silu(g) * u.float()
