@@ -1,0 +1,256 @@
+"""Headline benchmark: output tok/s of Llama-3-8B serving, 64 concurrent requests of 1024
+random input tokens generating 256 tokens each (ignore_eos), tensor parallel over the GPUs.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+    torchrun --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...
+
+One *step* is one full wave of the workload: all 64 requests are submitted at once and
+served to completion with continuous batching and chunked prefill (8192-token budget).
+``value`` is device-timed: CUDA events around exactly K waves, bracketed by a barrier and a
+synchronize on both sides, maximum over ranks.  ``e2e`` repeats the measurement through the
+public API (``LLM.generate`` with token-id prompts taken from pinned host memory; every
+engine step copies its inputs host->device and reads the sampled tokens device->host).
+Weights are random-init (N(0, 0.02)) with the exact Llama-3-8B shapes; inputs are uniform
+random token ids.  16 GB of weights are streamed every step, far more than L2 (126 MB).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "output tok/s per box (Llama-3-8B TP8, 1k in/256 out, conc 64); p50 TTFT, p50 TPOT"
+BASELINE_TOK_S = 184.44  # Llama-3.1-8B TP8 on trn2.48xlarge (published)
+
+LLAMA3_8B = {
+    "architectures": ["LlamaForCausalLM"], "model_type": "llama", "hidden_size": 4096,
+    "num_hidden_layers": 32, "num_attention_heads": 32, "num_key_value_heads": 8, "head_dim": 128,
+    "intermediate_size": 14336, "vocab_size": 128256, "rms_norm_eps": 1e-5, "rope_theta": 500000.0,
+    "max_position_embeddings": 8192, "tie_word_embeddings": False, "eos_token_id": 128001,
+}
+
+
+class ClockSampler:
+    """Samples SM clocks and throttle reasons with nvidia-smi while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.close()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    mx.append(float(parts[2]))
+                except ValueError:
+                    continue
+                for n, v in zip(names, parts[5:9]):
+                    if v.lower() == "active":
+                        reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def reference_arm(args):
+    """The reference (vllm-neuron) runs only on AWS Trainium through libtorch_neuronx_lite."""
+    why = None
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_dir, "vllm_neuron")):
+        why = "reference not installed under baseline/_ref"
+    else:
+        sys.path.insert(0, ref_dir)
+        try:
+            import vllm_neuron  # noqa: F401
+            why = ("vllm-neuron needs AWS Neuron devices and its libtorch_neuronx_lite/nkilib "
+                   "runtime (not in this image); it cannot execute on B200")
+        except Exception as e:
+            why = f"vllm-neuron import failed: {type(e).__name__}: {str(e)[:160]}"
+    rank = int(os.environ.get("RANK", "0"))
+    if rank == 0:
+        print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--num-prompts", type=int, default=64)
+    ap.add_argument("--input-len", type=int, default=1024)
+    ap.add_argument("--output-len", type=int, default=256)
+    ap.add_argument("--max-num-batched-tokens", type=int, default=8192)
+    ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--layers", type=int, default=None, help="debug only: fewer layers (invalid for reporting)")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return reference_arm(args)
+
+    import torch
+    import torch.distributed as dist
+
+    from vllm_neuron_b200.engine.sampling_params import SamplingParams
+    from vllm_neuron_b200.entrypoints import LLM
+    from vllm_neuron_b200.ops._ext import ext
+    from vllm_neuron_b200.parallel import state as ps
+
+    rank, world = ps.init_distributed(timeout_s=600)
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    cfg = dict(LLAMA3_8B)
+    if args.layers:
+        cfg["num_hidden_layers"] = args.layers
+    P, IN, OUT = args.num_prompts, args.input_len, args.output_len
+    max_len = IN + OUT + 16
+    blocks = P * ((max_len + 15) // 16) + 64
+    llm = LLM(cfg, tensor_parallel_size=world, max_num_seqs=P, max_model_len=max_len,
+              max_num_batched_tokens=args.max_num_batched_tokens, block_size=16, load_format="dummy",
+              num_gpu_blocks=blocks, seed=0, skip_tokenizer_init=True)
+    eng = llm.engine
+    sp = SamplingParams(temperature=0.0, max_tokens=OUT, ignore_eos=True)
+    g = torch.Generator().manual_seed(1234)
+    # Token-id prompts live in pinned host memory (one tensor per wave).
+    waves = [torch.randint(0, cfg["vocab_size"], (P, IN), generator=g, dtype=torch.int32).pin_memory()
+             for _ in range(2)]
+
+    def run_wave(i: int):
+        prompts = waves[i % 2].tolist()
+        t0 = time.perf_counter()
+        for j, p in enumerate(prompts):
+            eng.add_request(p, sp, request_id=f"w{i}-{j}", arrival_time=t0)
+        done = eng.run_until_done()
+        return done
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for i in range(args.warmup):
+        run_wave(i)
+    torch.cuda.synchronize()
+    barrier()
+
+    clocks = ClockSampler(int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local])
+                          if os.environ.get("CUDA_VISIBLE_DEVICES") else local)
+    clocks.start()
+    r0 = eng.runner
+    launches0 = ext().launch_count()
+    replayed0 = r0.replayed_kernels
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    barrier()
+    ev0.record()
+    ttft, tpot = [], []
+    for i in range(args.steps):
+        for r in run_wave(args.warmup + i):
+            ttft.append(r.first_token_time - r.arrival_time)
+            if len(r.output_token_ids) > 1:
+                tpot.append((r.finish_time - r.first_token_time) / (len(r.output_token_ids) - 1))
+    ev1.record()
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1)
+    gpu_launches = (ext().launch_count() - launches0) + (r0.replayed_kernels - replayed0)
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    tokens = args.steps * P * OUT
+    value = tokens / (ms / 1e3)
+
+    # ---- end to end through the public API
+    e2e = None
+    if not args.no_e2e:
+        K2 = args.e2e_steps or args.steps
+        h2d0, d2h0 = r0.h2d_bytes, r0.d2h_bytes
+        torch.cuda.synchronize()
+        barrier()
+        t0 = time.perf_counter()
+        for i in range(K2):
+            outs = llm.generate(waves[i % 2], sp)
+            assert len(outs) == P and all(len(o.outputs[0].token_ids) == OUT for o in outs)
+        torch.cuda.synchronize()
+        barrier()
+        dt = time.perf_counter() - t0
+        if world > 1:
+            t = torch.tensor([dt], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            dt = float(t.item())
+        e2e = {"value": K2 * P * OUT / dt, "unit": "tok/s",
+               "h2d_bytes_per_step": int((r0.h2d_bytes - h2d0) / K2),
+               "d2h_bytes_per_step": int((r0.d2h_bytes - d2h0) / K2),
+               "api": "vllm_neuron_b200.entrypoints.LLM.generate"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3),
+            "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": round(value / BASELINE_TOK_S, 3), "dtype": "bf16",
+            "data": "synthetic (uniform random token ids; random-init N(0,0.02) Llama-3-8B weights)",
+            "config": {"model": "Llama-3-8B architecture" + (f" ({args.layers} layers: DEBUG)" if args.layers else ""),
+                       "global_batch": P, "seq_len": IN + OUT, "input_len": IN, "output_len": OUT,
+                       "concurrency": P, "parallelism": f"tp{world}", "block_size": 16,
+                       "max_num_batched_tokens": args.max_num_batched_tokens,
+                       "l2": "inputs larger than L2 (16 GB of weights + KV streamed per step)"},
+            "p50_ttft_ms": round(float(np.median(ttft)) * 1e3, 2) if ttft else None,
+            "p50_tpot_ms": round(float(np.median(tpot)) * 1e3, 3) if tpot else None,
+            "clocks": clk, "e2e": e2e, "gpu_launches": int(gpu_launches),
+            "graph_replays": r0.num_graph_replays, "eager_steps": r0.num_eager_steps,
+        }
+        print(json.dumps(line), flush=True)
+    llm.shutdown()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -5,6 +5,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <atomic>
 #include <mutex>
 #include <unordered_map>
 
@@ -42,7 +43,12 @@ int64_t read_status() {
 }
 void reset_status() { TORCH_CHECK(cudaMemset(status_word(), 0, sizeof(uint32_t)) == cudaSuccess); }
 
-void check_launch(const char* what) {
+// Number of kernels this library has launched (or recorded into a CUDA graph) in this
+// process; the benchmark reports it for its timed region.
+std::atomic<int64_t> g_launches{0};
+
+void check_launch(const char* what, int kernels = 1) {
+  g_launches.fetch_add(kernels, std::memory_order_relaxed);
   const cudaError_t e = cudaGetLastError();
   TORCH_CHECK(e == cudaSuccess, what, " launch failed: ", cudaGetErrorString(e));
 }
@@ -131,7 +137,7 @@ void paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::T
   p.total_tokens = (int)q.size(0);
   const int num_work = (int)work.size(0);
   b200::paged_attention_launch(p, num_work, D, decode, cur_stream());
-  check_launch("paged_attention");
+  check_launch("paged_attention", num_work == 0 ? 0 : (num_splits > 1 ? 2 : 1));
 }
 
 void add_rmsnorm(at::Tensor& x, c10::optional<at::Tensor> residual, const at::Tensor& w,
@@ -165,9 +171,9 @@ void rope_kv_write(at::Tensor& qkv, const at::Tensor& positions,
   const c10::cuda::CUDAGuard guard(qkv.device());
   b200::RopeKvParams p{};
   p.positions = positions.data_ptr<int>();
-  p.slot_mapping = slot_mapping.has_value()
-                       ? reinterpret_cast<const long long*>(slot_mapping->data_ptr<int64_t>())
-                       : nullptr;
+  if (slot_mapping.has_value())
+    TORCH_CHECK(slot_mapping->scalar_type() == at::kInt, "slot_mapping must be int32");
+  p.slot_mapping = slot_mapping.has_value() ? slot_mapping->data_ptr<int>() : nullptr;
   p.cos_sin = cos_sin.data_ptr<float>();
   p.qkv_stride = qkv.stride(0);
   p.q_out = reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr());
@@ -256,6 +262,7 @@ void argmax(const at::Tensor& logits, at::Tensor& out_idx, c10::optional<at::Ten
 }
 
 int64_t num_sms() { return b200::num_sms_cached(); }
+int64_t launch_count() { return g_launches.load(); }
 
 }  // namespace
 
@@ -272,4 +279,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("read_status", &read_status);
   m.def("reset_status", &reset_status);
   m.def("num_sms", &num_sms);
+  m.def("launch_count", &launch_count);
 }

@@ -13,7 +13,7 @@ void add_rmsnorm_launch(void* x, bool x_is_f32, long long x_stride, __nv_bfloat1
 
 struct RopeKvParams {
   const int* positions;        // [T]
-  const long long* slot_mapping;  // [T] or null (no cache write)
+  const int* slot_mapping;     // [T] int32 or null (no cache write); < 0 skips
   const float* cos_sin;        // [max_pos, rot_dim]: cos in [0, rot/2), sin in [rot/2, rot)
   long long qkv_stride;        // row stride of the qkv input (elements)
   __nv_bfloat16* q_out;

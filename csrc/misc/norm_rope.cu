@@ -129,7 +129,7 @@ __global__ void __launch_bounds__(256) rope_kv_write_kernel(const RopeKvParams p
   const int D = p.head_dim;
   const int half = p.rot_dim / 2;
   const int pos = p.positions[t];
-  const long long slot = p.slot_mapping ? p.slot_mapping[t] : -1;
+  const long long slot = p.slot_mapping ? (long long)p.slot_mapping[t] : -1;
   const float* cs = p.cos_sin + (long long)pos * p.rot_dim;  // [cos(half) | sin(half)]
   const int nheads = p.Hq + 2 * p.Hkv;
   TIN* row = qkv + t * p.qkv_stride;

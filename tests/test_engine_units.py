@@ -1,0 +1,103 @@
+"""Host-side units: config parsing, block manager, scheduler policy, group rank math."""
+import pytest
+
+from vllm_neuron_b200.config import B200Config, ModelArchConfig
+from vllm_neuron_b200.engine.block_manager import BlockManager
+from vllm_neuron_b200.engine.request import Request
+from vllm_neuron_b200.engine.sampling_params import SamplingParams
+from vllm_neuron_b200.engine.scheduler import Scheduler, bucket_for
+from vllm_neuron_b200.parallel import state as ps
+
+
+def test_b200_config_accepts_reference_keys():
+    c = B200Config.from_additional_config({"neuron_config": {
+        "ep_degree": 8, "attention_dp_size": 2, "num_batched_tokens_buckets": [512, 128, 256],
+        "on_device_sampling_config": {"global_topk": 64}, "quantization": "fp8", "unknown_key": 1}})
+    assert c.ep_degree == 8 and c.attention_dp_size == 2
+    assert c.num_batched_tokens_buckets == [128, 256, 512]
+    assert c.on_device_sampling_config.global_topk == 64 and c.on_device_sampling_config.enabled
+    assert c.extra == {"unknown_key": 1}
+    assert B200Config.from_additional_config({"b200_config": {"mlp_dp_size": 2}}).mlp_dp_size == 2
+    with pytest.raises(ValueError):
+        B200Config.from_dict({"attention_dp_size": 0})
+    with pytest.raises(ValueError):
+        B200Config.from_dict({"quantization": "int3"})
+    assert not B200Config.from_dict({"on_device_sampling_config": None}).on_device_sampling_config.enabled
+
+
+def test_arch_config_rope_formats():
+    a = ModelArchConfig.from_hf({"rope_parameters": {"rope_theta": 500000.0, "rope_type": "default"},
+                                 "hidden_size": 256, "num_attention_heads": 4})
+    assert a.rope_theta == 500000.0 and a.rope_scaling is None and a.head_dim == 64
+    b = ModelArchConfig.from_hf({"rope_theta": 1e6, "rope_scaling": {"rope_type": "llama3", "factor": 8.0}})
+    assert b.rope_theta == 1e6 and b.rope_scaling["factor"] == 8.0
+    c = ModelArchConfig.from_hf({"rope_parameters": {"rope_theta": 150000.0, "rope_type": "yarn", "factor": 32.0}})
+    assert c.rope_scaling["rope_type"] == "yarn"
+
+
+def _req(rid, n, max_tokens=4):
+    return Request(rid, list(range(1, n + 1)), SamplingParams(temperature=0, max_tokens=max_tokens, ignore_eos=True))
+
+
+def test_block_manager_alloc_free_and_prefix_cache():
+    bm = BlockManager(10, 4, enable_prefix_caching=True)
+    r = _req("a", 10)
+    assert bm.allocate(r, 10) and len(r.block_ids) == 3 and 0 not in r.block_ids
+    r.num_computed_tokens = 10
+    bm.commit_full_blocks(r)
+    bm.free_request(r)
+    assert bm.num_free_blocks == 9
+    r2 = _req("b", 10)
+    assert bm.match_prefix(r2) == 8  # two full blocks reused
+    assert bm.allocate(r2, 10) and len(r2.block_ids) == 3
+    big = _req("c", 40)
+    assert not bm.allocate(big, 40)  # all-or-nothing
+    assert len(big.block_ids) == 0
+
+
+def test_scheduler_chunked_prefill_and_decode_mix():
+    bm = BlockManager(100, 16)
+    s = Scheduler(bm, max_num_seqs=4, max_num_batched_tokens=50, max_model_len=512)
+    a, b = _req("a", 40), _req("b", 40)
+    s.add_request(a)
+    s.add_request(b)
+    o1 = s.schedule()
+    assert [(x.req.request_id, x.num_tokens, x.samples) for x in o1.scheduled] == [("a", 40, True), ("b", 10, False)]
+    s.update(o1, [7])
+    o2 = s.schedule()
+    assert [(x.req.request_id, x.num_tokens) for x in o2.scheduled] == [("a", 1), ("b", 30)]
+    s.update(o2, [8, 9])
+    assert a.output_token_ids == [7, 8] and b.output_token_ids == [9]
+
+
+def test_scheduler_no_mixing_mode():
+    bm = BlockManager(100, 16)
+    s = Scheduler(bm, max_num_seqs=4, max_num_batched_tokens=500, max_model_len=512, mixed_batches=False)
+    a, b = _req("a", 20), _req("b", 20)
+    s.add_request(a)
+    o1 = s.schedule()
+    s.update(o1, [1])
+    s.add_request(b)
+    o2 = s.schedule()
+    kinds = {x.num_tokens == 1 for x in o2.scheduled}
+    assert len(kinds) == 1  # never prefill and decode together
+
+
+def test_bucket_for():
+    assert bucket_for([128, 256, 512], 1) == 128
+    assert bucket_for([128, 256, 512], 300) == 512
+    assert bucket_for([128], 600) == 600
+    assert bucket_for(None, 7) == 7
+
+
+def test_parallel_group_math():
+    assert ps.tp_groups(8, 4) == [[0, 1, 2, 3], [4, 5, 6, 7]]
+    assert ps.dp_groups(8, 4) == [[0, 4], [1, 5], [2, 6], [3, 7]]
+    assert ps.ep_groups(8, 8) == [list(range(8))]
+    assert ps.ep_tp_groups(8, 4) == [[0, 4], [1, 5], [2, 6], [3, 7]]
+    inner, outer = ps.sub_groups(list(range(8)), 2)
+    assert inner == [[0, 1], [2, 3], [4, 5], [6, 7]] and outer == [[0, 2, 4, 6], [1, 3, 5, 7]]
+    kv, head = ps.dcp_groups(list(range(8)), 2)
+    assert kv == [[0, 4], [1, 5], [2, 6], [3, 7]] and head == [[0, 1, 2, 3], [4, 5, 6, 7]]
+    with pytest.raises(ValueError):
+        ps.ParallelConfig(world_size=8, tensor_parallel_size=3, data_parallel_size=1).validate()

@@ -151,7 +151,7 @@ def test_rope_kv_write(cuda_device, D, neox, qknorm, f32_in):
     qkv = torch.randn(T, (Hq + 2 * Hkv) * D, device=cuda_device, dtype=dt)
     qkv_cpu = qkv.detach().cpu().clone()
     pos = torch.randint(0, 4000, (T,), dtype=torch.int32, device=cuda_device)
-    slots = torch.randperm(nb * bs)[:T].to(torch.int64)
+    slots = torch.randperm(nb * bs)[:T].to(torch.int32)
     slots[3] = -1
     slots = slots.to(cuda_device)
     tab = ops.cos_sin_table(4096, D, 500000.0, device=cuda_device)

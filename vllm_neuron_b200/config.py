@@ -72,6 +72,13 @@ class ModelArchConfig:
         nh = cfg.get("num_attention_heads", 32)
         head_dim = cfg.get("head_dim") or H // nh
         qcfg = cfg.get("quantization_config") or {}
+        # transformers >= 5 keeps theta and scaling under "rope_parameters"; older configs
+        # use top-level "rope_theta" / "rope_scaling".
+        rp = cfg.get("rope_parameters") or {}
+        rope_theta = cfg.get("rope_theta", rp.get("rope_theta", 10000.0))
+        rope_scaling = cfg.get("rope_scaling")
+        if rope_scaling is None and rp and rp.get("rope_type", "default") != "default":
+            rope_scaling = dict(rp)
         c = cls(
             model_type=cfg.get("model_type", "llama"),
             architectures=tuple(cfg.get("architectures") or ("LlamaForCausalLM",)),
@@ -83,9 +90,9 @@ class ModelArchConfig:
             intermediate_size=cfg.get("intermediate_size", 4 * H),
             vocab_size=cfg.get("vocab_size", 32000),
             rms_norm_eps=cfg.get("rms_norm_eps", 1e-5),
-            rope_theta=cfg.get("rope_theta", 10000.0),
-            rope_scaling=cfg.get("rope_scaling"),
-            partial_rotary_factor=cfg.get("partial_rotary_factor", 1.0),
+            rope_theta=rope_theta,
+            rope_scaling=rope_scaling,
+            partial_rotary_factor=cfg.get("partial_rotary_factor", rp.get("partial_rotary_factor", 1.0)),
             max_position_embeddings=cfg.get("max_position_embeddings", 8192),
             tie_word_embeddings=cfg.get("tie_word_embeddings", False),
             qk_norm=cfg.get("model_type", "") in ("qwen3", "qwen3_moe", "qwen3_next", "qwen3_vl"),

@@ -1,0 +1,166 @@
+"""In-process serving engine: scheduler + model runner + request bookkeeping.
+
+Tensor parallelism is SPMD: every rank (one process per GPU) runs the same deterministic
+scheduler on the same requests; sampled tokens are identical on all ranks because every rank
+samples the full-vocabulary logits with the same seeds, so no per-step broadcast is needed.
+"""
+from __future__ import annotations
+
+import itertools
+import time
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from ..config import B200Config, ModelArchConfig
+from ..metrics import Metrics
+from ..parallel.comm import SINGLE, GroupComm
+from .block_manager import BlockManager
+from .request import Request, RequestStatus
+from .sampling_params import SamplingParams
+from .scheduler import Scheduler
+
+
+@dataclass
+class EngineArgs:
+    model: str | dict | None = None
+    max_num_seqs: int = 256
+    max_num_batched_tokens: int = 8192
+    max_model_len: int | None = None
+    block_size: int = 16
+    gpu_memory_utilization: float = 0.9
+    num_gpu_blocks: int | None = None
+    enable_prefix_caching: bool = False
+    enable_chunked_prefill: bool = True
+    load_format: str = "auto"      # "auto" | "dummy"
+    seed: int = 0
+    dtype: str = "bfloat16"
+    device: str = "cuda"
+    cuda_graphs: bool = True
+    additional_config: dict = field(default_factory=dict)
+
+
+@dataclass
+class CompletionOutput:
+    index: int
+    token_ids: list[int]
+    text: str = ""
+    logprobs: list[float] | None = None
+    finish_reason: str | None = None
+
+
+@dataclass
+class RequestOutput:
+    request_id: str
+    prompt_token_ids: list[int]
+    outputs: list[CompletionOutput]
+    finished: bool
+    metrics: dict = field(default_factory=dict)
+
+
+class LLMEngine:
+    def __init__(self, args: EngineArgs, tp: GroupComm = SINGLE):
+        from ..models import registry
+        from ..utils.checkpoints import load_checkpoint_into
+        from ..worker.model_runner import ModelRunner
+
+        self.args = args
+        self.tp = tp
+        self.b200_config = B200Config.from_additional_config(args.additional_config)
+        self.model_path = None
+        if isinstance(args.model, dict):
+            self.arch = ModelArchConfig.from_hf(args.model)
+        elif isinstance(args.model, ModelArchConfig):
+            self.arch = args.model
+        else:
+            self.model_path = args.model
+            self.arch = ModelArchConfig.from_path(args.model)
+        self.max_model_len = args.max_model_len or self.arch.max_position_embeddings
+        self.device = torch.device(args.device)
+        if self.device.type == "cuda" and self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
+        dtype = {"bfloat16": torch.bfloat16, "float32": torch.float32, "float16": torch.float16}[args.dtype]
+        cls = registry.resolve(self.arch.architectures)
+        max_tok = max(args.max_num_batched_tokens, args.max_num_seqs)
+        self.model = cls(self.arch, tp=tp, device=self.device, dtype=dtype, max_tokens=max_tok,
+                         max_seqs=args.max_num_seqs, block_size=args.block_size)
+        if args.load_format == "dummy" or self.model_path is None:
+            self.model.init_random(seed=args.seed)
+        else:
+            load_checkpoint_into(self.model, self.model_path)
+        self.runner = ModelRunner(self.model, max_num_seqs=args.max_num_seqs,
+                                  max_num_batched_tokens=max_tok, max_model_len=self.max_model_len,
+                                  block_size=args.block_size,
+                                  cuda_graphs=args.cuda_graphs and self.b200_config.cuda_graphs,
+                                  device=self.device, seed=args.seed)
+        nb = args.num_gpu_blocks or self.runner.profile_num_blocks(args.gpu_memory_utilization)
+        if tp.world > 1 and self.device.type == "cuda":
+            t = torch.tensor([nb], dtype=torch.int64, device=self.device)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MIN, group=tp.group)
+            nb = int(t.item())
+        self.runner.allocate_kv_cache(nb)
+        self.metrics = Metrics()
+        self.block_manager = BlockManager(nb, args.block_size, args.enable_prefix_caching)
+        self.scheduler = Scheduler(self.block_manager, args.max_num_seqs, max_tok, self.max_model_len,
+                                   enable_chunked_prefill=args.enable_chunked_prefill,
+                                   num_batched_tokens_buckets=self.b200_config.num_batched_tokens_buckets,
+                                   num_seqs_buckets=self.b200_config.num_seqs_buckets,
+                                   metrics=self.metrics)
+        self.runner.capture_graphs()
+        self._ids = itertools.count()
+        self.eos_token_id = self.arch.raw.get("eos_token_id")
+        if isinstance(self.eos_token_id, list):
+            self.eos_token_id = self.eos_token_id[0] if self.eos_token_id else None
+        self.num_steps = 0
+
+    # ---------------------------------------------------------------- requests
+    def add_request(self, prompt_token_ids: list[int], params: SamplingParams | None = None,
+                    request_id: str | None = None, arrival_time: float | None = None) -> str:
+        params = SamplingParams.coerce(params)
+        rid = request_id if request_id is not None else str(next(self._ids))
+        req = Request(rid, list(prompt_token_ids), params, eos_token_id=self.eos_token_id)
+        if arrival_time is not None:
+            req.arrival_time = arrival_time
+        self.scheduler.add_request(req)
+        return rid
+
+    def abort_request(self, request_id: str):
+        self.scheduler.abort_request(request_id)
+
+    def has_unfinished_requests(self) -> bool:
+        return self.scheduler.has_unfinished()
+
+    # ---------------------------------------------------------------- stepping
+    def step(self) -> list[Request]:
+        out = self.scheduler.schedule()
+        if out.empty:
+            return []
+        want_lp = any(s.req.sampling_params.logprobs for s in out.scheduled if s.samples)
+        toks, lps = self.runner.execute(out, want_logprobs=want_lp)
+        now = time.perf_counter()
+        finished = self.scheduler.update(out, toks, lps, now=now)
+        self.num_steps += 1
+        self.metrics.steps += 1
+        return finished
+
+    def run_until_done(self) -> list[Request]:
+        done = []
+        while self.scheduler.has_unfinished():
+            done.extend(self.step())
+        return done
+
+    @staticmethod
+    def to_output(req: Request) -> RequestOutput:
+        reason = {RequestStatus.FINISHED_STOPPED: "stop", RequestStatus.FINISHED_LENGTH: "length",
+                  RequestStatus.FINISHED_ABORTED: "abort"}.get(req.status)
+        m = {"arrival_time": req.arrival_time, "first_token_time": req.first_token_time,
+             "finish_time": req.finish_time, "num_cached_tokens": req.num_cached_tokens}
+        return RequestOutput(req.request_id, req.prompt_token_ids,
+                             [CompletionOutput(0, list(req.output_token_ids),
+                                               logprobs=req.output_logprobs or None,
+                                               finish_reason=reason)],
+                             req.status.finished, m)
+
+    def shutdown(self):
+        self.runner.release_graphs()

@@ -1,0 +1,99 @@
+"""Offline inference API: ``LLM(model, ...).generate(prompts, sampling_params)``.
+
+Mirrors the ``vllm.LLM`` call surface the reference's users rely on
+(examples/vllm_neuron/models/llama3/run.py: ``LLM(model=..., tensor_parallel_size=...,
+additional_config={"neuron_config": {...}})``).  Under ``torchrun`` each rank constructs the
+same ``LLM``; tensor parallelism spans the ranks and every rank returns the outputs.
+``model`` is a local HF directory, or a HF ``config.json`` dict (random-init weights).
+"""
+from __future__ import annotations
+
+import os
+from typing import Any, Iterable
+
+import torch
+
+from ..engine.llm_engine import EngineArgs, LLMEngine, RequestOutput
+from ..engine.sampling_params import SamplingParams
+from ..parallel import state as ps
+
+
+def _normalize_prompt(p: Any, tokenizer) -> list[int]:
+    if isinstance(p, dict):
+        if "prompt_token_ids" in p:
+            return list(p["prompt_token_ids"])
+        if "prompt" in p:
+            p = p["prompt"]
+    if hasattr(p, "prompt_token_ids"):
+        return list(p.prompt_token_ids)
+    if isinstance(p, str):
+        if tokenizer is None:
+            raise ValueError("text prompts need a tokenizer; pass token ids or a model dir with one")
+        return list(tokenizer.encode(p))
+    if isinstance(p, torch.Tensor):
+        return p.tolist()
+    return [int(x) for x in p]
+
+
+class LLM:
+    def __init__(self, model, tensor_parallel_size: int = 1, max_num_seqs: int = 256,
+                 max_model_len: int | None = None, max_num_batched_tokens: int = 8192,
+                 block_size: int = 16, gpu_memory_utilization: float = 0.9,
+                 enable_prefix_caching: bool = False, load_format: str = "auto", seed: int = 0,
+                 additional_config: dict | None = None, tokenizer: str | None = None,
+                 skip_tokenizer_init: bool = False, num_gpu_blocks: int | None = None,
+                 enforce_eager: bool = False, device: str | None = None, dtype: str = "auto",
+                 **unused):
+        if device is None:
+            device = f"cuda:{torch.cuda.current_device()}" if torch.cuda.is_available() else "cpu"
+        ps.init_distributed(backend="gloo" if str(device).startswith("cpu") else None)
+        world = torch.distributed.get_world_size() if torch.distributed.is_initialized() else 1
+        if tensor_parallel_size != world and world > 1:
+            raise ValueError(f"tensor_parallel_size={tensor_parallel_size} but {world} ranks were launched")
+        st = ps.initialize_parallel_state(ps.ParallelConfig(world_size=world,
+                                                            tensor_parallel_size=tensor_parallel_size))
+        if dtype == "auto":
+            dtype = "bfloat16" if str(device).startswith("cuda") else "float32"
+        args = EngineArgs(model=model, max_num_seqs=max_num_seqs,
+                          max_num_batched_tokens=max_num_batched_tokens, max_model_len=max_model_len,
+                          block_size=block_size, gpu_memory_utilization=gpu_memory_utilization,
+                          num_gpu_blocks=num_gpu_blocks, enable_prefix_caching=enable_prefix_caching,
+                          load_format=load_format, seed=seed, dtype=dtype, device=device,
+                          cuda_graphs=not enforce_eager, additional_config=additional_config or {})
+        self.engine = LLMEngine(args, tp=st.tp)
+        self.tokenizer = None
+        if not skip_tokenizer_init:
+            path = tokenizer or (model if isinstance(model, str) else None)
+            if path and any(os.path.exists(os.path.join(path, f)) for f in
+                            ("tokenizer.json", "tokenizer.model", "tokenizer_config.json")):
+                from transformers import AutoTokenizer
+
+                self.tokenizer = AutoTokenizer.from_pretrained(path)
+
+    def get_tokenizer(self):
+        return self.tokenizer
+
+    def generate(self, prompts, sampling_params: SamplingParams | list | None = None,
+                 use_tqdm: bool = False) -> list[RequestOutput]:
+        if isinstance(prompts, (str, dict)) or (isinstance(prompts, list) and prompts and isinstance(prompts[0], int)):
+            prompts = [prompts]
+        prompts = list(prompts)
+        if not isinstance(sampling_params, list):
+            sampling_params = [sampling_params] * len(prompts)
+        ids = []
+        base = self.engine.num_steps * 1_000_003
+        for i, (p, sp) in enumerate(zip(prompts, sampling_params)):
+            toks = _normalize_prompt(p, self.tokenizer)
+            ids.append(self.engine.add_request(toks, sp, request_id=f"gen-{base}-{i}"))
+        done = {r.request_id: r for r in self.engine.run_until_done()}
+        outs = []
+        for rid in ids:
+            o = LLMEngine.to_output(done[rid])
+            if self.tokenizer is not None:
+                for c in o.outputs:
+                    c.text = self.tokenizer.decode(c.token_ids, skip_special_tokens=True)
+            outs.append(o)
+        return outs
+
+    def shutdown(self):
+        self.engine.shutdown()

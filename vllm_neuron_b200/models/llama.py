@@ -42,7 +42,7 @@ class ForwardBatch:
 
     input_ids: torch.Tensor      # [T] int32
     positions: torch.Tensor      # [T] int32
-    slot_mapping: torch.Tensor   # [T] int64 (-1 = do not write)
+    slot_mapping: torch.Tensor   # [T] int32 (-1 = do not write)
     block_tables: torch.Tensor   # [B, max_blocks] int32
     seq_lens: torch.Tensor       # [B] int32
     q_start: torch.Tensor        # [B + 1] int32

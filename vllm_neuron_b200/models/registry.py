@@ -1,0 +1,27 @@
+"""Architecture name -> model class (reference: vllm_neuron/model/registry.py:11-38)."""
+from __future__ import annotations
+
+import importlib
+
+_MODELS = {
+    "LlamaForCausalLM": ("vllm_neuron_b200.models.llama", "LlamaForCausalLM"),
+    "MistralForCausalLM": ("vllm_neuron_b200.models.llama", "LlamaForCausalLM"),
+    "Qwen3ForCausalLM": ("vllm_neuron_b200.models.llama", "LlamaForCausalLM"),
+    "Qwen2ForCausalLM": ("vllm_neuron_b200.models.llama", "LlamaForCausalLM"),
+}
+
+
+def register_model(arch: str, module: str, cls: str):
+    _MODELS[arch] = (module, cls)
+
+
+def get_models() -> dict[str, tuple[str, str]]:
+    return dict(_MODELS)
+
+
+def resolve(arch_names) -> type:
+    for a in arch_names:
+        if a in _MODELS:
+            mod, cls = _MODELS[a]
+            return getattr(importlib.import_module(mod), cls)
+    raise ValueError(f"unsupported architectures {list(arch_names)}; supported: {sorted(_MODELS)}")

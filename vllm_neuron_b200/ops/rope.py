@@ -85,7 +85,7 @@ def rope_kv_write(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Ten
                   rot_dim: int | None = None, neox: bool = True,
                   clear_input: bool = False) -> torch.Tensor:
     """Rotate q/k of ``qkv [T, (Hq + 2 Hkv) * D]``; write rotated q to ``q_out [T, Hq * D]`` and
-    k/v into the paged cache at ``slot_mapping`` (int64, negative = skip)."""
+    k/v into the paged cache at ``slot_mapping`` (int32, negative = skip)."""
     rot_dim = rot_dim or head_dim
     if not qkv.is_cuda:
         rope_kv_write_ref(qkv, positions, cos_sin, num_q_heads, num_kv_heads, head_dim, q_out,

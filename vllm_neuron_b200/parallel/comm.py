@@ -26,6 +26,7 @@ class GroupComm:
             self.rank = dist.get_rank(group)
             self.world = dist.get_world_size(group)
             self.ranks = ranks if ranks is not None else list(range(self.world))
+        self.is_gloo = group is not None and dist.is_initialized() and dist.get_backend(group) == "gloo"
 
     @property
     def is_single(self) -> bool:
@@ -40,6 +41,14 @@ class GroupComm:
         if self.world == 1:
             return t
         t = t.contiguous()
+        if self.is_gloo:
+            parts = [torch.empty_like(t) for _ in range(self.world)]
+            dist.all_gather(parts, t, group=self.group)
+            res = torch.cat(parts, dim=dim)
+            if out is not None:
+                out.copy_(res)
+                return out
+            return res
         if dim == 0:
             if out is None:
                 out = torch.empty((t.shape[0] * self.world,) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
@@ -60,6 +69,11 @@ class GroupComm:
             return t
         if out is None:
             out = torch.empty((t.shape[0] // self.world,) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+        if self.is_gloo:
+            full = t.contiguous().clone()
+            dist.all_reduce(full, group=self.group)
+            out.copy_(full.chunk(self.world, 0)[self.rank])
+            return out
         dist.reduce_scatter_tensor(out, t.contiguous(), group=self.group)
         return out
 

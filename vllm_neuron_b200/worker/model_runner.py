@@ -1,0 +1,339 @@
+"""Model runner: batch preparation, KV-cache ownership, CUDA graphs and on-device sampling.
+
+Per step the host builds every int/float input of the forward pass and of the sampler in
+ONE pinned int32 buffer (floats are stored as their bit patterns), copies it to the device
+with one ``cudaMemcpyAsync``, and views the sections on the device.  Pure-decode batches
+replay a CUDA graph captured per batch-size bucket (padded rows write nothing to the cache:
+slot -1, null block 0); prefill and mixed batches run eagerly.  The sampled token ids come
+back with one device->host copy into pinned memory.
+
+Reference: NeuronModelRunner (vllm_neuron/vllm/worker/neuron_model_runner.py): input prep
+:2605-3057, attention metadata :4084-4258, KV cache allocation :8456-8619, per-bucket graph
+compile + warm-up :4437-5094 (CUDA graphs per bucket here), on-device sampling :5717-6054.
+"""
+from __future__ import annotations
+
+import math
+import time
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from .. import ops
+from ..engine.scheduler import SchedulerOutput
+from ..models.llama import ForwardBatch
+
+_ALIGN = 4  # int32 elements (16 bytes) between sections
+
+
+def _round(n: int) -> int:
+    return (n + _ALIGN - 1) // _ALIGN * _ALIGN
+
+
+@dataclass
+class Layout:
+    """Section offsets (int32 elements) inside the packed input buffer."""
+
+    T: int
+    B: int
+    S: int
+    W: int
+    nblk: int
+
+    def __post_init__(self):
+        o = 0
+        self.off = {}
+        for name, n in (("ids", self.T), ("pos", self.T), ("slot", self.T), ("qstart", self.B + 1),
+                        ("seqlen", self.B), ("lidx", self.S), ("work", 2 * self.W),
+                        ("bt", self.B * self.nblk), ("temp", self.S), ("topk", self.S),
+                        ("topp", self.S), ("minp", self.S), ("seed", 2 * self.S), ("offs", self.S)):
+            self.off[name] = (o, n)
+            o += _round(n)
+        self.total = o
+
+
+class ModelRunner:
+    def __init__(self, model, *, max_num_seqs: int, max_num_batched_tokens: int, max_model_len: int,
+                 block_size: int = 16, cuda_graphs: bool = True, graph_buckets: list[int] | None = None,
+                 device="cuda", seed: int = 0):
+        self.model = model
+        self.device = torch.device(device)
+        self.is_cuda = self.device.type == "cuda"
+        self.max_num_seqs = max_num_seqs
+        self.max_tokens = max_num_batched_tokens
+        self.max_model_len = max_model_len
+        self.block_size = block_size
+        self.max_blocks = (max_model_len + block_size - 1) // block_size
+        self.use_graphs = cuda_graphs and self.is_cuda
+        cap = min(max_num_seqs, model.max_decode_tokens)
+        self.graph_buckets = sorted(b for b in (graph_buckets or [1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128])
+                                    if b <= cap)
+        if cap not in self.graph_buckets and cap > 0:
+            self.graph_buckets.append(cap)
+        self.graphs: dict[int, tuple] = {}
+        self.seed = seed
+        self.num_sms = torch.cuda.get_device_properties(self.device).multi_processor_count if self.is_cuda else 148
+        max_layout = Layout(self.max_tokens, max_num_seqs, max_num_seqs, self._max_work(), self.max_blocks)
+        pin = self.is_cuda
+        self.host_buf = torch.zeros(max_layout.total, dtype=torch.int32, pin_memory=pin)
+        self.dev_buf = torch.zeros(max_layout.total, dtype=torch.int32, device=self.device)
+        self.host_np = self.host_buf.numpy()
+        self.tok_host = torch.zeros(max_num_seqs, dtype=torch.int32, pin_memory=pin)
+        self.lp_host = torch.zeros(max_num_seqs, dtype=torch.float32, pin_memory=pin)
+        self.tok_dev = torch.zeros(max_num_seqs, dtype=torch.int32, device=self.device)
+        self.lp_dev = torch.zeros(max_num_seqs, dtype=torch.float32, device=self.device)
+        self.h2d_bytes = 0
+        self.d2h_bytes = 0
+        self.num_graph_replays = 0
+        self.num_eager_steps = 0
+        self.graph_kernels: dict[int, int] = {}  # kernels recorded per captured bucket
+        self.replayed_kernels = 0
+        self.kv_cache = None
+
+    def _max_work(self) -> int:
+        # prefill work items: ceil(q_len * G / 64) per sequence, bounded by tokens*G/64 + seqs
+        G = max(1, self.model.Hq // self.model.Hkv)
+        return self.max_tokens * G // ops.attention.PREFILL_ROWS + self.max_num_seqs + 1
+
+    # ------------------------------------------------------------------ KV cache
+    def kv_bytes_per_block(self) -> int:
+        return self.model.kv_bytes_per_block()
+
+    def allocate_kv_cache(self, num_blocks: int):
+        m = self.model
+        shape = (m.cfg.num_layers, 2) + m.kv_cache_shape(num_blocks)
+        self.kv_cache = torch.zeros(shape, dtype=m.dtype, device=self.device)
+        m.bind_kv_cache([(self.kv_cache[i, 0], self.kv_cache[i, 1]) for i in range(m.cfg.num_layers)])
+        self.num_blocks = num_blocks
+
+    def profile_num_blocks(self, gpu_memory_utilization: float, reserve_bytes: int = 2 << 30) -> int:
+        """Blocks that fit in ``utilization * total`` after weights and workspaces."""
+        if not self.is_cuda:
+            return 4096
+        torch.cuda.synchronize(self.device)
+        free, total = torch.cuda.mem_get_info(self.device)
+        used = total - free
+        budget = total * gpu_memory_utilization - used - reserve_bytes
+        n = int(budget // self.kv_bytes_per_block())
+        if n < 2:
+            raise RuntimeError(f"not enough memory for the KV cache (budget {budget / 2**30:.2f} GiB)")
+        return n
+
+    # ------------------------------------------------------------------ input packing
+    def _pack(self, out: SchedulerOutput, lay: Layout, pad_B: int | None = None) -> tuple[int, bool, int]:
+        """Fill the pinned buffer for ``out``.  Returns (#sampling rows, decode?, num_splits)."""
+        h = self.host_np
+        o = lay.off
+        sch = out.scheduled
+        B = len(sch)
+        Bp = pad_B or B
+        m = self.model
+        bs = self.block_size
+        ids = h[o["ids"][0]:o["ids"][0] + lay.T]
+        pos = h[o["pos"][0]:o["pos"][0] + lay.T]
+        slot = h[o["slot"][0]:o["slot"][0] + lay.T]
+        qst = h[o["qstart"][0]:o["qstart"][0] + Bp + 1]
+        sl = h[o["seqlen"][0]:o["seqlen"][0] + Bp]
+        bt = h[o["bt"][0]:o["bt"][0] + Bp * lay.nblk].reshape(Bp, lay.nblk)
+        lidx = h[o["lidx"][0]:o["lidx"][0] + lay.S]
+        t = 0
+        s = 0
+        q_lens = np.zeros(Bp, dtype=np.int64)
+        temp = h[o["temp"][0]:o["temp"][0] + lay.S].view(np.float32)
+        topk = h[o["topk"][0]:o["topk"][0] + lay.S]
+        topp = h[o["topp"][0]:o["topp"][0] + lay.S].view(np.float32)
+        minp = h[o["minp"][0]:o["minp"][0] + lay.S].view(np.float32)
+        seed = h[o["seed"][0]:o["seed"][0] + 2 * lay.S].view(np.int64)
+        offs = h[o["offs"][0]:o["offs"][0] + lay.S]
+        for i, sr in enumerate(sch):
+            req = sr.req
+            n = sr.num_tokens
+            st = sr.start
+            P = req.num_prompt_tokens
+            if st >= P:
+                ids[t:t + n] = req.output_token_ids[st - P:st - P + n]
+            elif st + n <= P:
+                ids[t:t + n] = req.prompt_token_ids[st:st + n]
+            else:
+                ids[t:t + n] = (req.prompt_token_ids + req.output_token_ids)[st:st + n]
+            p = np.arange(st, st + n, dtype=np.int32)
+            pos[t:t + n] = p
+            blocks = np.asarray(req.block_ids, dtype=np.int32)
+            slot[t:t + n] = blocks[p // bs] * bs + (p % bs)
+            qst[i] = t
+            sl[i] = st + n
+            q_lens[i] = n
+            nb = len(req.block_ids)
+            bt[i, :nb] = blocks
+            bt[i, nb:] = 0
+            t += n
+            if sr.samples:
+                lidx[s] = t - 1
+                sp = req.sampling_params
+                temp[s] = 0.0 if sp.greedy else sp.temperature
+                topk[s] = sp.top_k or 0
+                topp[s] = sp.top_p if sp.top_p is not None else 1.0
+                minp[s] = sp.min_p or 0.0
+                seed[s] = sp.seed if sp.seed is not None else (hash(req.request_id) ^ self.seed) & 0x7FFFFFFFFFFF
+                offs[s] = len(req.output_token_ids)
+                s += 1
+        # padding rows (graph buckets): one token each, no cache write, null block
+        for i in range(B, Bp):
+            ids[t] = 0
+            pos[t] = 0
+            slot[t] = -1
+            qst[i] = t
+            sl[i] = 1
+            q_lens[i] = 1
+            bt[i, :] = 0
+            lidx[s] = t
+            temp[s] = 0.0
+            topk[s] = 0
+            topp[s] = 1.0
+            minp[s] = 0.0
+            seed[s] = 0
+            offs[s] = 0
+            t += 1
+            s += 1
+        qst[Bp] = t
+        G = max(1, m.Hq // m.Hkv)
+        if pad_B is not None:
+            w = ops.build_work(np.ones(Bp, dtype=np.int64), np.full(Bp, self.max_model_len), G, m.Hkv, self.num_sms,
+                               max_splits=m.attn_splits_max)
+        else:
+            w = ops.build_work(q_lens[:Bp], sl[:Bp].astype(np.int64), G, m.Hkv, self.num_sms,
+                               max_splits=m.attn_splits_max)
+        work = h[o["work"][0]:o["work"][0] + 2 * len(w.work)]
+        work[:] = w.work.reshape(-1)
+        self._last_work_len = len(w.work)
+        return s, w.decode, w.num_splits
+
+    def _views(self, buf: torch.Tensor, lay: Layout, B: int, S: int, W: int, decode: bool, splits: int) -> tuple:
+        o = lay.off
+
+        def sec(name, n, dtype=None):
+            a = buf[o[name][0]:o[name][0] + n]
+            return a.view(dtype) if dtype is not None else a
+
+        nb = lay.nblk
+        fb = ForwardBatch(
+            input_ids=sec("ids", lay.T), positions=sec("pos", lay.T), slot_mapping=sec("slot", lay.T),
+            block_tables=sec("bt", B * nb).view(B, nb), seq_lens=sec("seqlen", B),
+            q_start=sec("qstart", B + 1), work=sec("work", 2 * W).view(W, 2),
+            logits_indices=sec("lidx", S),
+            decode=decode, num_splits=splits, num_tokens=lay.T)
+        samp = dict(temperature=sec("temp", S, torch.float32), top_k=sec("topk", S),
+                    top_p=sec("topp", S, torch.float32), min_p=sec("minp", S, torch.float32),
+                    seeds=sec("seed", 2 * S).view(torch.int64), offsets=sec("offs", S))
+        return fb, samp
+
+    def _forward_and_sample(self, fb: ForwardBatch, samp: dict, S: int, tok_out: torch.Tensor,
+                            lp_out: torch.Tensor | None):
+        logits = self.model.forward(fb)
+        ops.sample(logits, samp["temperature"], samp["top_k"], samp["top_p"], samp["seeds"],
+                   samp["offsets"], min_p=samp["min_p"], out=tok_out[:S],
+                   out_logprob=lp_out[:S] if lp_out is not None else None)
+
+    # ------------------------------------------------------------------ graphs
+    def capture_graphs(self):
+        if not self.use_graphs:
+            return
+        m = self.model
+        torch.cuda.synchronize(self.device)
+        pool = torch.cuda.graph_pool_handle()
+        stream = torch.cuda.Stream(self.device)
+        for b in sorted(self.graph_buckets, reverse=True):
+            lay = Layout(b, b, b, b, self.max_blocks)
+            buf = torch.zeros(lay.total, dtype=torch.int32, device=self.device)
+            G = max(1, m.Hq // m.Hkv)
+            w = ops.build_work(np.ones(b, dtype=np.int64), np.full(b, self.max_model_len), G, m.Hkv,
+                               self.num_sms, max_splits=m.attn_splits_max)
+            # valid dummy metadata for the warm-up / capture runs
+            h = torch.zeros(lay.total, dtype=torch.int32)
+            o = lay.off
+            h[o["qstart"][0]:o["qstart"][0] + b + 1] = torch.arange(b + 1, dtype=torch.int32)
+            h[o["seqlen"][0]:o["seqlen"][0] + b] = 1
+            h[o["slot"][0]:o["slot"][0] + b] = -1
+            h[o["lidx"][0]:o["lidx"][0] + b] = torch.arange(b, dtype=torch.int32)
+            h[o["work"][0]:o["work"][0] + 2 * b] = torch.from_numpy(w.work.reshape(-1))
+            h[o["topp"][0]:o["topp"][0] + b] = torch.tensor([1.0] * b).view(torch.int32)
+            buf.copy_(h)
+            fb, samp = self._views(buf, lay, b, b, b, True, w.num_splits)
+            tok = torch.zeros(b, dtype=torch.int32, device=self.device)
+            lp = torch.zeros(b, dtype=torch.float32, device=self.device)
+            stream.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(stream):
+                for _ in range(2):
+                    self._forward_and_sample(fb, samp, b, tok, lp)
+            torch.cuda.current_stream(self.device).wait_stream(stream)
+            torch.cuda.synchronize(self.device)
+            g = torch.cuda.CUDAGraph()
+            n0 = ops._ext.ext().launch_count()
+            with torch.cuda.graph(g, pool=pool, stream=stream):
+                self._forward_and_sample(fb, samp, b, tok, lp)
+            self.graph_kernels[b] = ops._ext.ext().launch_count() - n0
+            torch.cuda.synchronize(self.device)
+            self.graphs[b] = (g, lay, buf, tok, lp, w.num_splits)
+
+    def release_graphs(self):
+        self.graphs.clear()
+
+    # ------------------------------------------------------------------ execute
+    def execute(self, out: SchedulerOutput, want_logprobs: bool = False) -> tuple[np.ndarray, np.ndarray | None]:
+        """Run one step; returns sampled tokens (and logprobs) of the sampling rows in order."""
+        B = len(out.scheduled)
+        if B == 0:
+            return np.zeros(0, dtype=np.int32), None
+        if out.num_tokens > self.max_tokens:
+            raise ValueError(f"batch of {out.num_tokens} tokens exceeds max_num_batched_tokens")
+        S = sum(1 for s in out.scheduled if s.samples)
+        bucket = None
+        if self.use_graphs and out.is_pure_decode and self.graphs:
+            for bb in sorted(self.graphs):
+                if bb >= B:
+                    bucket = bb
+                    break
+        if bucket is not None:
+            g, lay, buf, tok, lp, splits = self.graphs[bucket]
+            self._pack(out, lay, pad_B=bucket)
+            n = lay.total
+            buf.copy_(self.host_buf[:n], non_blocking=True)
+            self.h2d_bytes += n * 4
+            g.replay()
+            self.num_graph_replays += 1
+            self.replayed_kernels += self.graph_kernels.get(bucket, 0)
+            tok_src, lp_src = tok, lp
+        else:
+            lay = Layout(out.num_tokens, B, S, self._max_work_for(out), self.max_blocks)
+            S2, decode, splits = self._pack(out, lay)
+            W = self._last_work_len
+            n = lay.total
+            dev = self.dev_buf[:n]
+            dev.copy_(self.host_buf[:n], non_blocking=self.is_cuda)
+            self.h2d_bytes += n * 4
+            fb, samp = self._views(dev, lay, B, S, W, decode, splits)
+            fb.work = fb.work[:W]
+            if S > 0:
+                self._forward_and_sample(fb, samp, S, self.tok_dev, self.lp_dev)
+            else:
+                self.model.forward(fb)
+            self.num_eager_steps += 1
+            tok_src, lp_src = self.tok_dev, self.lp_dev
+        if S == 0:
+            return np.zeros(0, dtype=np.int32), None
+        self.tok_host[:S].copy_(tok_src[:S], non_blocking=self.is_cuda)
+        self.d2h_bytes += S * 4
+        if want_logprobs:
+            self.lp_host[:S].copy_(lp_src[:S], non_blocking=self.is_cuda)
+            self.d2h_bytes += S * 4
+        if self.is_cuda:
+            torch.cuda.current_stream(self.device).synchronize()
+        toks = self.tok_host[:S].numpy().copy()
+        lps = self.lp_host[:S].numpy().copy() if want_logprobs else None
+        return toks, lps
+
+    def _max_work_for(self, out: SchedulerOutput) -> int:
+        m = self.model
+        G = max(1, m.Hq // m.Hkv)
+        return sum(math.ceil(s.num_tokens * G / ops.attention.PREFILL_ROWS) for s in out.scheduled) + 1
