@@ -1,0 +1,138 @@
+"""Device time of one serving step of Llama-3-8B (random weights) on one GPU, without host
+overhead: a decode step of B sequences at context L replayed from its CUDA graph, and one
+eager prefill chunk of T tokens.  Also reports the host time of batch preparation.
+
+    python benchmarks/bench_step.py [--batch 64] [--ctx 1152] [--chunk 8192] [--layers 32]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import time
+
+import numpy as np
+import torch
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+from bench import LLAMA3_8B  # noqa: E402
+from vllm_neuron_b200.engine.request import Request  # noqa: E402
+from vllm_neuron_b200.engine.sampling_params import SamplingParams  # noqa: E402
+from vllm_neuron_b200.engine.scheduler import ScheduledRequest, SchedulerOutput  # noqa: E402
+from vllm_neuron_b200.entrypoints import LLM  # noqa: E402
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--ctx", type=int, default=1152)
+    ap.add_argument("--chunk", type=int, default=8192)
+    ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--json", type=str, default=None)
+    ap.add_argument("--profile-once", action="store_true",
+                    help="run one decode replay and one prefill chunk inside NVTX ranges "
+                         "'decode_step' / 'prefill_chunk' (for an ncu launch list)")
+    a = ap.parse_args()
+    cfg = dict(LLAMA3_8B, num_hidden_layers=a.layers)
+    B, L = a.batch, a.ctx
+    max_len = max(L + 64, 2048)
+    blocks = B * (max_len // 16 + 1) + 64
+    llm = LLM(cfg, max_num_seqs=B, max_model_len=max_len, max_num_batched_tokens=a.chunk,
+              load_format="dummy", num_gpu_blocks=blocks, skip_tokenizer_init=True)
+    eng = llm.engine
+    runner = eng.runner
+    sp = SamplingParams(temperature=0.0, max_tokens=1 << 20, ignore_eos=True)
+    # Fake B running requests at context L with contiguous block ids.
+    reqs = []
+    nb = (L + 1 + 15) // 16
+    for i in range(B):
+        r = Request(str(i), list(np.random.randint(0, 1000, L)), sp)
+        r.output_token_ids = [1]
+        r.num_computed_tokens = L
+        r.block_ids = list(range(1 + i * nb, 1 + (i + 1) * nb))
+        reqs.append(r)
+    out = SchedulerOutput([ScheduledRequest(r, L, 1, True) for r in reqs], B)
+    res = {}
+    if a.profile_once:
+        bucket = min(b for b in runner.graphs if b >= B)
+        g = runner.graphs[bucket][0]
+        lay_b, buf_b = runner.graphs[bucket][1], runner.graphs[bucket][2]
+        runner._pack(out, lay_b, pad_B=bucket)
+        buf_b.copy_(runner.host_buf[:lay_b.total])
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("decode_step")
+        g.replay()
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
+        T = a.chunk
+        n_seq = max(1, T // 1024)
+        per = T // n_seq
+        nb2 = (per + 15) // 16
+        preqs = []
+        for i in range(n_seq):
+            r = Request("p%d" % i, list(np.random.randint(0, 1000, per)), sp)
+            r.block_ids = list(range(1 + i * nb2, 1 + (i + 1) * nb2))
+            preqs.append(r)
+        pout = SchedulerOutput([ScheduledRequest(r, 0, per, True) for r in preqs], per * n_seq)
+        torch.cuda.nvtx.range_push("prefill_chunk")
+        runner.execute(pout)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
+        print("profile-once done", flush=True)
+        return
+    # host preparation cost
+    t0 = time.perf_counter()
+    for _ in range(50):
+        runner.execute(out)
+    torch.cuda.synchronize()
+    res["decode_step_with_host_ms"] = (time.perf_counter() - t0) / 50 * 1e3
+    g, lay, buf, tok, lp, splits = runner.graphs[min(b for b in runner.graphs if b >= B)]
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.iters):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    res["decode_step_gpu_ms"] = e0.elapsed_time(e1) / a.iters
+    res["attn_splits"] = splits
+    t0 = time.perf_counter()
+    for _ in range(200):
+        runner._pack(out, lay, pad_B=min(b for b in runner.graphs if b >= B))
+    res["pack_host_ms"] = (time.perf_counter() - t0) / 200 * 1e3
+    # prefill chunk
+    T = a.chunk
+    n_seq = max(1, T // 1024)
+    per = T // n_seq
+    preqs = []
+    nb2 = (per + 15) // 16
+    for i in range(n_seq):
+        r = Request("p%d" % i, list(np.random.randint(0, 1000, per)), sp)
+        r.block_ids = list(range(1 + i * nb2, 1 + (i + 1) * nb2))
+        preqs.append(r)
+    pout = SchedulerOutput([ScheduledRequest(r, 0, per, True) for r in preqs], per * n_seq)
+    runner.execute(pout)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(3):
+        runner.execute(pout)
+    e1.record()
+    torch.cuda.synchronize()
+    res["prefill_chunk_ms"] = e0.elapsed_time(e1) / 3
+    res["prefill_tokens"] = per * n_seq
+    flops = 2 * 7.5e9 * per * n_seq * a.layers / 32
+    res["prefill_tflops_dense_only"] = flops / (res["prefill_chunk_ms"] * 1e9)
+    res.update(batch=B, ctx=L, layers=a.layers)
+    print(json.dumps(res), flush=True)
+    if a.json:
+        with open(a.json, "w") as f:
+            json.dump(res, f)
+
+
+if __name__ == "__main__":
+    main()

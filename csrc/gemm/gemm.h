@@ -22,7 +22,7 @@ struct GemmArgs {
   int M, N, K;
   int bn;         // N tile: 16/32/64/128/256
   int epi;        // GemmEpilogue
-  int splits;     // split-K factor (needs an fp32 reduction epilogue when > 1)
+  int splits;     // split-K factor (fp32 reduction epilogue when > 1); < 0 = stream-K
   int group_m;    // rasterization group along M (0 = default)
   int max_ctas;   // cap on persistent CTAs (0 = number of SMs)
   uint32_t* status;  // device status word for bounded-wait failures (may be null)

@@ -42,6 +42,7 @@ struct GemmParams {
   int M, N, K;
   int num_m_blocks, num_n_blocks, num_k_blocks;
   int splits, kb_per_split;
+  int streamk;  // 1: each CTA owns an equal contiguous range of (tile, k-block) units
   int group_m;
   void* out;
   long long ldo;
@@ -61,6 +62,41 @@ __device__ __forceinline__ void decode_tile(const GemmParams& p, int tile, int& 
   mb = first_m + r % gm;
   nb = r / gm;
 }
+
+// Work segments of one CTA: (tile, k-block range).  All three roles walk the same sequence.
+struct SegCursor {
+  long long u, u_end;
+  int tile;
+  __device__ explicit SegCursor(const GemmParams& p) {
+    if (p.streamk) {
+      const long long U = (long long)p.num_m_blocks * p.num_n_blocks * p.num_k_blocks;
+      u = U * blockIdx.x / gridDim.x;
+      u_end = U * (blockIdx.x + 1) / gridDim.x;
+      tile = 0;
+    } else {
+      u = u_end = 0;
+      tile = blockIdx.x;
+    }
+  }
+  __device__ bool next(const GemmParams& p, int& mb, int& nb, int& k0, int& k1) {
+    int split;
+    if (p.streamk) {
+      if (u >= u_end) return false;
+      const int t = (int)(u / p.num_k_blocks);
+      k0 = (int)(u - (long long)t * p.num_k_blocks);
+      k1 = (int)min((long long)p.num_k_blocks, k0 + (u_end - u));
+      u += k1 - k0;
+      decode_tile(p, t, mb, nb, split);
+      return true;
+    }
+    if (tile >= p.num_m_blocks * p.num_n_blocks * p.splits) return false;
+    decode_tile(p, tile, mb, nb, split);
+    k0 = split * p.kb_per_split;
+    k1 = min(k0 + p.kb_per_split, p.num_k_blocks);
+    tile += gridDim.x;
+    return true;
+  }
+};
 
 template <int BN>
 struct TmemCols {
@@ -118,8 +154,6 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_base_smem;
 
-  const int total_tiles = p.num_m_blocks * p.num_n_blocks * p.splits;
-
   if (warp == 0) {
     // ------------------------------ TMA producer ------------------------------
     if (elect_one()) {
@@ -131,11 +165,9 @@ __global__ void __launch_bounds__(192, 1)
                                   : policy_evict_first();
       uint32_t it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
-        int mb, nb, split;
-        decode_tile(p, tile, mb, nb, split);
-        const int k0 = split * p.kb_per_split;
-        const int k1 = min(k0 + p.kb_per_split, p.num_k_blocks);
+      SegCursor cur(p);
+      int mb, nb, k0, k1;
+      while (ok && cur.next(p, mb, nb, k0, k1)) {
         for (int kb = k0; kb < k1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
@@ -161,11 +193,9 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t it = 0;
       int t_local = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x, ++t_local) {
-        int mb, nb, split;
-        decode_tile(p, tile, mb, nb, split);
-        const int k0 = split * p.kb_per_split;
-        const int k1 = min(k0 + p.kb_per_split, p.num_k_blocks);
+      SegCursor cur(p);
+      int mb, nb, k0, k1;
+      for (; ok && cur.next(p, mb, nb, k0, k1); ++t_local) {
         const int acc = t_local & 1;
         const uint32_t aph = (t_local >> 1) & 1;
         if (!mbar_wait_abortable(&tempty_bar[acc], aph ^ 1, kTimeoutTmemEmpty, p.status, abort_flag)) {
@@ -200,9 +230,9 @@ __global__ void __launch_bounds__(192, 1)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int row = q * 32 + lane;
     int t_local = 0;
-    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++t_local) {
-      int mb, nb, split;
-      decode_tile(p, tile, mb, nb, split);
+    SegCursor cur(p);
+    int mb, nb, k0, k1;
+    for (; cur.next(p, mb, nb, k0, k1); ++t_local) {
       const int acc = t_local & 1;
       const uint32_t aph = (t_local >> 1) & 1;
       if (!mbar_wait_abortable(&tfull_bar[acc], aph, kTimeoutTmemFull, p.status, abort_flag)) break;
@@ -392,20 +422,26 @@ void gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
   p.num_n_blocks = (a.N + bn - 1) / bn;
   if (a.epi == EPI_SILU_BF16) p.num_n_blocks = (a.N + bn - 1) / bn;  // N = 2 * I (interleaved)
   p.num_k_blocks = (a.K + kBK - 1) / kBK;
+  p.streamk = a.splits < 0 ? 1 : 0;
   int splits = a.splits < 1 ? 1 : a.splits;
   if (splits > p.num_k_blocks) splits = p.num_k_blocks;
   p.kb_per_split = (p.num_k_blocks + splits - 1) / splits;
   p.splits = (p.num_k_blocks + p.kb_per_split - 1) / p.kb_per_split;  // no empty split
-  if (p.splits > 1 && (a.epi != EPI_F32_RED && a.epi != EPI_F32_RED_T))
-    throw std::invalid_argument("gemm: split-K requires an fp32 reduction epilogue");
+  if ((p.splits > 1 || p.streamk) && (a.epi != EPI_F32_RED && a.epi != EPI_F32_RED_T))
+    throw std::invalid_argument("gemm: split-K / stream-K require an fp32 reduction epilogue");
   p.group_m = a.group_m > 0 ? a.group_m : 16;
   p.out = a.out;
   p.ldo = a.ldo;
   p.status = a.status;
-  const int tiles = p.num_m_blocks * p.num_n_blocks * p.splits;
+  const long long tiles = (long long)p.num_m_blocks * p.num_n_blocks * p.splits;
   int grid = num_sms_cached();
   if (a.max_ctas > 0 && a.max_ctas < grid) grid = a.max_ctas;
-  if (tiles < grid) grid = tiles;
+  if (p.streamk) {
+    const long long units = (long long)p.num_m_blocks * p.num_n_blocks * p.num_k_blocks;
+    if (units < grid) grid = (int)units;
+  } else if (tiles < grid) {
+    grid = (int)tiles;
+  }
 
 #define B200_GEMM_CASE(BN_, ST_, EPI_)                                    \
   if (bn == BN_ && a.epi == EPI_) {                                       \

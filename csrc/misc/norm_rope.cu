@@ -55,8 +55,44 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 
 }  // namespace
 
-// One CTA per row; each thread keeps its slice of the row in registers (H <= 8 * 8 * 256).
-template <typename TX, bool HAS_RES>
+// One CTA per row.  Thread t owns 8-element vectors t, t + blockDim, ... (NV of them, a
+// compile-time count, so the row slice stays in registers).
+template <typename TX>
+__device__ __forceinline__ void load8(const TX* p, float (&v)[8]);
+template <>
+__device__ __forceinline__ void load8<float>(const float* p, float (&v)[8]) {
+  const float4 a = reinterpret_cast<const float4*>(p)[0];
+  const float4 b = reinterpret_cast<const float4*>(p)[1];
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+template <>
+__device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* p, float (&v)[8]) {
+  const uint4 a = *reinterpret_cast<const uint4*>(p);
+  const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = unpack_bf16x2(w[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void store8_bf16(__nv_bfloat16* p, const float (&v)[8]) {
+  *reinterpret_cast<uint4*>(p) = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]),
+                                            pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+}
+template <typename TX>
+__device__ __forceinline__ void zero8(TX* p);
+template <>
+__device__ __forceinline__ void zero8<float>(float* p) {
+  reinterpret_cast<float4*>(p)[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+  reinterpret_cast<float4*>(p)[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+}
+template <>
+__device__ __forceinline__ void zero8<__nv_bfloat16>(__nv_bfloat16* p) {
+  *reinterpret_cast<uint4*>(p) = make_uint4(0, 0, 0, 0);
+}
+
+template <typename TX, bool HAS_RES, int NV>
 __global__ void __launch_bounds__(256) add_rmsnorm_kernel(TX* x, long long x_stride,
                                                           __nv_bfloat16* residual,
                                                           long long r_stride,
@@ -64,32 +100,66 @@ __global__ void __launch_bounds__(256) add_rmsnorm_kernel(TX* x, long long x_str
                                                           __nv_bfloat16* out, long long o_stride,
                                                           int H, float eps, bool clear_x) {
   __shared__ float red[32];
-  const int row = blockIdx.x;
+  const long long row = blockIdx.x;
   TX* xr = x + row * x_stride;
   __nv_bfloat16* rr = HAS_RES ? residual + row * r_stride : nullptr;
-  constexpr int kMaxPer = 32;  // elements per thread
-  float v[kMaxPer];
+  float v[NV][8];
   float ss = 0.f;
-  int n = 0;
-  for (int i = threadIdx.x; i < H; i += blockDim.x, ++n) {
-    float a = to_f(xr[i]);
-    if (HAS_RES) {
-      a += __bfloat162float(rr[i]);
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int idx = (j * blockDim.x + threadIdx.x) * 8;
+    if (idx < H) {
+      load8<TX>(xr + idx, v[j]);
+      if (HAS_RES) {
+        float r[8];
+        load8<__nv_bfloat16>(rr + idx, r);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          // round the new residual to bf16 (the stored value) before normalising it
+          v[j][e] = __bfloat162float(__float2bfloat16(v[j][e] + r[e]));
+        }
+        store8_bf16(rr + idx, v[j]);
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss += v[j][e] * v[j][e];
+      if (clear_x) zero8<TX>(xr + idx);
     }
-    v[n] = a;
-    ss += a * a;
   }
   ss = block_sum(ss, red);
   const float inv = rsqrtf(ss / (float)H + eps);
-  n = 0;
-  for (int i = threadIdx.x; i < H; i += blockDim.x, ++n) {
-    const __nv_bfloat16 rb = __float2bfloat16(v[n]);
-    if (HAS_RES) rr[i] = rb;
-    // Normalize the bf16-rounded residual, as the unfused bf16 model would.
-    const float a = HAS_RES ? __bfloat162float(rb) : v[n];
-    out[row * o_stride + i] = __float2bfloat16(a * inv * __bfloat162float(w[i]));
-    if (clear_x) xr[i] = from_f<TX>(0.f);
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int idx = (j * blockDim.x + threadIdx.x) * 8;
+    if (idx < H) {
+      float g[8], o[8];
+      load8<__nv_bfloat16>(w + idx, g);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = v[j][e] * inv * g[e];
+      store8_bf16(out + row * o_stride + idx, o);
+    }
   }
+}
+
+template <typename TX, bool HAS_RES>
+static void launch_norm(TX* x, long long xs, __nv_bfloat16* res, long long rs,
+                        const __nv_bfloat16* w, __nv_bfloat16* out, long long os, int rows, int H,
+                        float eps, bool clear, cudaStream_t stream) {
+  const int vecs = H / 8;
+  int threads = vecs <= 128 ? ((vecs + 31) / 32) * 32 : (vecs <= 512 ? 128 : 256);
+  const int nv = (vecs + threads - 1) / threads;
+#define B200_NORM(NV_)                                                                   \
+  if (nv <= NV_) {                                                                       \
+    add_rmsnorm_kernel<TX, HAS_RES, NV_><<<rows, threads, 0, stream>>>(x, xs, res, rs, w, \
+                                                                         out, os, H, eps, \
+                                                                         clear);          \
+    return;                                                                              \
+  }
+  B200_NORM(1)
+  B200_NORM(2)
+  B200_NORM(4)
+  B200_NORM(8)
+#undef B200_NORM
+  throw std::invalid_argument("add_rmsnorm: hidden size too large");
 }
 
 void add_rmsnorm_launch(void* x, bool x_is_f32, long long x_stride, __nv_bfloat16* residual,
@@ -97,23 +167,21 @@ void add_rmsnorm_launch(void* x, bool x_is_f32, long long x_stride, __nv_bfloat1
                         long long o_stride, int rows, int H, float eps, bool clear_x,
                         cudaStream_t stream) {
   if (rows == 0) return;
-  if (H > 256 * 32) throw std::invalid_argument("add_rmsnorm: hidden size too large");
-  const int threads = H >= 2048 ? 256 : 128;
-  if (H > threads * 32) throw std::invalid_argument("add_rmsnorm: hidden size too large");
+  if (H % 8 != 0) throw std::invalid_argument("add_rmsnorm: hidden size must be a multiple of 8");
   if (x_is_f32) {
     if (residual)
-      add_rmsnorm_kernel<float, true><<<rows, threads, 0, stream>>>(
-          (float*)x, x_stride, residual, r_stride, w, out, o_stride, H, eps, clear_x);
+      launch_norm<float, true>((float*)x, x_stride, residual, r_stride, w, out, o_stride, rows,
+                               H, eps, clear_x, stream);
     else
-      add_rmsnorm_kernel<float, false><<<rows, threads, 0, stream>>>(
-          (float*)x, x_stride, residual, r_stride, w, out, o_stride, H, eps, clear_x);
+      launch_norm<float, false>((float*)x, x_stride, residual, r_stride, w, out, o_stride, rows,
+                                H, eps, clear_x, stream);
   } else {
     if (residual)
-      add_rmsnorm_kernel<__nv_bfloat16, true><<<rows, threads, 0, stream>>>(
-          (__nv_bfloat16*)x, x_stride, residual, r_stride, w, out, o_stride, H, eps, false);
+      launch_norm<__nv_bfloat16, true>((__nv_bfloat16*)x, x_stride, residual, r_stride, w, out,
+                                       o_stride, rows, H, eps, false, stream);
     else
-      add_rmsnorm_kernel<__nv_bfloat16, false><<<rows, threads, 0, stream>>>(
-          (__nv_bfloat16*)x, x_stride, residual, r_stride, w, out, o_stride, H, eps, false);
+      launch_norm<__nv_bfloat16, false>((__nv_bfloat16*)x, x_stride, residual, r_stride, w, out,
+                                        o_stride, rows, H, eps, false, stream);
   }
 }
 
@@ -122,73 +190,95 @@ void add_rmsnorm_launch(void* x, bool x_is_f32, long long x_stride, __nv_bfloat1
 // Input row layout: [q heads | k heads | v heads] * D.  The rotated q is written to q_out
 // (bf16, may alias the input when the input is bf16).
 // ------------------------------------------------------------------------------------------
-template <typename TIN>
+template <typename TIN, int D>
 __global__ void __launch_bounds__(256) rope_kv_write_kernel(const RopeKvParams p, TIN* qkv) {
+  constexpr int PER = D / 32;  // elements per lane: lane l owns l, l + 32, l + 64, ...
   const int t = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int D = p.head_dim;
   const int half = p.rot_dim / 2;
   const int pos = p.positions[t];
   const long long slot = p.slot_mapping ? (long long)p.slot_mapping[t] : -1;
   const float* cs = p.cos_sin + (long long)pos * p.rot_dim;  // [cos(half) | sin(half)]
   const int nheads = p.Hq + 2 * p.Hkv;
-  TIN* row = qkv + t * p.qkv_stride;
+  TIN* row = qkv + (long long)t * p.qkv_stride;
   for (int h = warp; h < nheads; h += blockDim.x >> 5) {
     const bool is_q = h < p.Hq;
     const bool is_k = !is_q && h < p.Hq + p.Hkv;
     TIN* src = row + (long long)h * D;
-    // Each lane handles up to 8 elements (D <= 256).
-    float v[8];
-    const int per = D / 32;
-    for (int e = 0; e < per; ++e) v[e] = to_f(src[lane + 32 * e]);
+    float v[PER];
+#pragma unroll
+    for (int e = 0; e < PER; ++e) v[e] = to_f(src[lane + 32 * e]);
     if ((is_q && p.q_norm_w) || (is_k && p.k_norm_w)) {
       float ss = 0.f;
-      for (int e = 0; e < per; ++e) ss += v[e] * v[e];
+#pragma unroll
+      for (int e = 0; e < PER; ++e) ss += v[e] * v[e];
       ss = warp_sum(ss);
       const float inv = rsqrtf(ss / (float)D + p.eps);
       const __nv_bfloat16* nw = is_q ? p.q_norm_w : p.k_norm_w;
-      for (int e = 0; e < per; ++e) {
-        // round to bf16 like a standalone norm followed by rope would
+#pragma unroll
+      for (int e = 0; e < PER; ++e)
         v[e] = __bfloat162float(__float2bfloat16(v[e] * inv * __bfloat162float(nw[lane + 32 * e])));
-      }
     }
     if (is_q || is_k) {
-      // Rotate pairs.  neox: (i, i + half); interleaved: (2i, 2i + 1).  Gather partners via
-      // shared-nothing shuffles: write to a small per-warp smem line instead.
-      __shared__ float line[8][256];
-      float* L = line[warp & 7];
-      for (int e = 0; e < per; ++e) L[lane + 32 * e] = v[e];
-      __syncwarp();
-      for (int e = 0; e < per; ++e) {
-        const int i = lane + 32 * e;
-        if (i >= p.rot_dim) continue;
-        float out;
-        if (p.neox) {
+      if (p.neox && p.rot_dim == D && PER >= 2) {
+        // Full-width neox rotation: pair (i, i + D/2) lives in one lane, elements e, e + PER/2.
+        constexpr int HP = PER / 2;
+        float o[PER];
+#pragma unroll
+        for (int e = 0; e < HP; ++e) {
+          const int i = lane + 32 * e;
+          const float c = cs[i], s = cs[D / 2 + i];
+          o[e] = v[e] * c - v[e + HP] * s;
+          o[e + HP] = v[e + HP] * c + v[e] * s;
+        }
+#pragma unroll
+        for (int e = 0; e < PER; ++e) v[e] = o[e];
+      } else if (!p.neox) {
+        // Interleaved pairs (2j, 2j + 1) sit in neighbouring lanes.
+#pragma unroll
+        for (int e = 0; e < PER; ++e) {
+          const int i = lane + 32 * e;
+          const float other = __shfl_xor_sync(0xffffffffu, v[e], 1);
+          if (i < p.rot_dim) {
+            const int j = i >> 1;
+            const float c = cs[j], s = cs[half + j];
+            v[e] = (i & 1) ? v[e] * c + other * s : v[e] * c - other * s;
+          }
+        }
+      } else {
+        // neox with a rotary width that is not a multiple of 64: exchange through smem.
+        __shared__ float line[8][256];
+        float* Ls = line[warp & 7];
+#pragma unroll
+        for (int e = 0; e < PER; ++e) Ls[lane + 32 * e] = v[e];
+        __syncwarp();
+#pragma unroll
+        for (int e = 0; e < PER; ++e) {
+          const int i = lane + 32 * e;
+          if (i >= p.rot_dim) continue;
           const int j = i < half ? i : i - half;
           const float c = cs[j], s = cs[half + j];
-          out = i < half ? L[i] * c - L[i + half] * s : L[i] * c + L[i - half] * s;
-        } else {
-          const int j = i >> 1;
-          const float c = cs[j], s = cs[half + j];
-          out = (i & 1) ? L[i] * c + L[i - 1] * s : L[i] * c - L[i + 1] * s;
+          v[e] = i < half ? Ls[i] * c - Ls[i + half] * s : Ls[i] * c + Ls[i - half] * s;
         }
-        v[e] = out;
+        __syncwarp();
       }
-      __syncwarp();
     }
     if (is_q) {
-      __nv_bfloat16* dst = p.q_out + t * p.q_out_stride + (long long)h * D;
-      for (int e = 0; e < per; ++e) dst[lane + 32 * e] = __float2bfloat16(v[e]);
+      __nv_bfloat16* dst = p.q_out + (long long)t * p.q_out_stride + (long long)h * D;
+#pragma unroll
+      for (int e = 0; e < PER; ++e) dst[lane + 32 * e] = __float2bfloat16(v[e]);
     } else if (slot >= 0) {
       const int kvh = is_k ? h - p.Hq : h - p.Hq - p.Hkv;
       const long long blk = slot / p.block_size, off = slot % p.block_size;
       __nv_bfloat16* cache = is_k ? p.k_cache : p.v_cache;
       __nv_bfloat16* dst =
           cache + blk * p.kv_block_stride + ((long long)kvh * p.block_size + off) * D;
-      for (int e = 0; e < per; ++e) dst[lane + 32 * e] = __float2bfloat16(v[e]);
+#pragma unroll
+      for (int e = 0; e < PER; ++e) dst[lane + 32 * e] = __float2bfloat16(v[e]);
     }
     if (p.clear_input) {
-      for (int e = 0; e < per; ++e) src[lane + 32 * e] = from_f<TIN>(0.f);
+#pragma unroll
+      for (int e = 0; e < PER; ++e) src[lane + 32 * e] = from_f<TIN>(0.f);
     }
   }
 }
@@ -196,46 +286,77 @@ __global__ void __launch_bounds__(256) rope_kv_write_kernel(const RopeKvParams p
 void rope_kv_write_launch(const RopeKvParams& p, void* qkv, bool qkv_is_f32, int T,
                           cudaStream_t stream) {
   if (T == 0) return;
-  if (p.head_dim % 32 != 0 || p.head_dim > 256)
-    throw std::invalid_argument("rope_kv_write: head_dim must be a multiple of 32, <= 256");
-  if (qkv_is_f32)
-    rope_kv_write_kernel<float><<<T, 256, 0, stream>>>(p, (float*)qkv);
-  else
-    rope_kv_write_kernel<__nv_bfloat16><<<T, 256, 0, stream>>>(p, (__nv_bfloat16*)qkv);
+#define B200_ROPE(D_)                                                                       \
+  if (p.head_dim == D_) {                                                                   \
+    if (qkv_is_f32)                                                                         \
+      rope_kv_write_kernel<float, D_><<<T, 256, 0, stream>>>(p, (float*)qkv);               \
+    else                                                                                    \
+      rope_kv_write_kernel<__nv_bfloat16, D_><<<T, 256, 0, stream>>>(p, (__nv_bfloat16*)qkv); \
+    return;                                                                                 \
+  }
+  B200_ROPE(64)
+  B200_ROPE(128)
+  B200_ROPE(256)
+#undef B200_ROPE
+  throw std::invalid_argument("rope_kv_write: head_dim must be 64, 128 or 256");
 }
 
 // ------------------------------------------------------------------------------------------
 // SiLU(gate) * up
 // ------------------------------------------------------------------------------------------
-template <typename TIN>
+template <typename TIN, int VEC>
 __global__ void silu_mul_kernel(TIN* in, long long in_stride, __nv_bfloat16* out,
                                 long long out_stride, int I, int blk, bool clear_input,
                                 float limit, float alpha, int act) {
-  const int t = blockIdx.y;
+  const long long t = blockIdx.y;
   TIN* r = in + t * in_stride;
-  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < I; j += gridDim.x * blockDim.x) {
-    int gi, ui;
-    if (blk > 0) {
-      const int b = j / blk, w = j % blk;
-      gi = b * 2 * blk + w;
-      ui = gi + blk;
-    } else {
-      gi = j;
-      ui = j + I;
+  const int j = (blockIdx.x * blockDim.x + threadIdx.x) * VEC;
+  if (j >= I) return;
+  int gi, ui;
+  if (blk > 0) {
+    const int b = j / blk, w = j % blk;
+    gi = b * 2 * blk + w;
+    ui = gi + blk;
+  } else {
+    gi = j;
+    ui = j + I;
+  }
+  float g[VEC], u[VEC], y[VEC];
+  if constexpr (VEC == 8) {
+    load8<TIN>(r + gi, g);
+    load8<TIN>(r + ui, u);
+  } else {
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) {
+      g[e] = to_f(r[gi + e]);
+      u[e] = to_f(r[ui + e]);
     }
-    float g = to_f(r[gi]), u = to_f(r[ui]);
-    float y;
+  }
+#pragma unroll
+  for (int e = 0; e < VEC; ++e) {
+    float gg = g[e], uu = u[e];
     if (act == 0) {  // SwiGLU
-      y = g / (1.f + __expf(-g)) * u;
+      y[e] = gg / (1.f + __expf(-gg)) * uu;
     } else {  // GPT-OSS clamped SwiGLU: (up + 1) * gate * sigmoid(alpha * gate)
-      g = fminf(g, limit);
-      u = fminf(fmaxf(u, -limit), limit);
-      y = (u + 1.f) * g / (1.f + __expf(-alpha * g));
+      gg = fminf(gg, limit);
+      uu = fminf(fmaxf(uu, -limit), limit);
+      y[e] = (uu + 1.f) * gg / (1.f + __expf(-alpha * gg));
     }
-    out[t * out_stride + j] = __float2bfloat16(y);
+  }
+  if constexpr (VEC == 8) {
+    store8_bf16(out + t * out_stride + j, y);
     if (clear_input) {
-      r[gi] = from_f<TIN>(0.f);
-      r[ui] = from_f<TIN>(0.f);
+      zero8<TIN>(r + gi);
+      zero8<TIN>(r + ui);
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) {
+      out[t * out_stride + j + e] = __float2bfloat16(y[e]);
+      if (clear_input) {
+        r[gi + e] = from_f<TIN>(0.f);
+        r[ui + e] = from_f<TIN>(0.f);
+      }
     }
   }
 }
@@ -244,13 +365,24 @@ void silu_mul_launch(void* in, bool in_is_f32, long long in_stride, __nv_bfloat1
                      long long out_stride, int T, int I, int blk, bool clear_input, int act,
                      float limit, float alpha, cudaStream_t stream) {
   if (T == 0) return;
-  dim3 grid((I + 255) / 256, T);
-  if (in_is_f32)
-    silu_mul_kernel<float><<<grid, 256, 0, stream>>>((float*)in, in_stride, out, out_stride, I,
-                                                     blk, clear_input, limit, alpha, act);
-  else
-    silu_mul_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
-        (__nv_bfloat16*)in, in_stride, out, out_stride, I, blk, false, limit, alpha, act);
+  const bool vec8 = (I % 8 == 0) && (blk % 8 == 0) && (in_stride % 8 == 0) && (out_stride % 8 == 0);
+  if (vec8) {
+    dim3 grid((I / 8 + 127) / 128, T);
+    if (in_is_f32)
+      silu_mul_kernel<float, 8><<<grid, 128, 0, stream>>>((float*)in, in_stride, out, out_stride, I,
+                                                          blk, clear_input, limit, alpha, act);
+    else
+      silu_mul_kernel<__nv_bfloat16, 8><<<grid, 128, 0, stream>>>(
+          (__nv_bfloat16*)in, in_stride, out, out_stride, I, blk, false, limit, alpha, act);
+  } else {
+    dim3 grid((I + 255) / 256, T);
+    if (in_is_f32)
+      silu_mul_kernel<float, 1><<<grid, 256, 0, stream>>>((float*)in, in_stride, out, out_stride, I,
+                                                          blk, clear_input, limit, alpha, act);
+    else
+      silu_mul_kernel<__nv_bfloat16, 1><<<grid, 256, 0, stream>>>(
+          (__nv_bfloat16*)in, in_stride, out, out_stride, I, blk, false, limit, alpha, act);
+  }
 }
 
 // ------------------------------------------------------------------------------------------

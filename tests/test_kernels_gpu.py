@@ -47,7 +47,10 @@ def test_gemm_skinny_and_splitk(cuda_device, M, N, K):
     out = L.gemm_skinny_bf16(x, w)
     assert _rel_err(out, ref) < 1e-2
     acc = torch.zeros(M, N, device=cuda_device, dtype=torch.float32)
-    L.gemm_accumulate(x, w, acc)
+    L.gemm_accumulate(x, w, acc)  # stream-K
+    assert _rel_err(acc, ref) < 1e-3
+    acc.zero_()
+    L.gemm_accumulate(x, w, acc, splits=3)  # fixed split-K
     assert _rel_err(acc, ref) < 1e-3
 
 
@@ -57,6 +60,9 @@ def test_gemm_accumulate_wide_splitk(cuda_device):
     w = torch.randn(N, K, device=cuda_device, dtype=torch.bfloat16) * 0.05
     acc = torch.zeros(M, N, device=cuda_device, dtype=torch.float32)
     L.gemm_accumulate(x, w, acc, splits=4)
+    assert _rel_err(acc, x.float() @ w.float().t()) < 1e-3
+    acc.zero_()
+    L.gemm_accumulate(x, w, acc)  # stream-K over wide tiles
     assert _rel_err(acc, x.float() @ w.float().t()) < 1e-3
 
 

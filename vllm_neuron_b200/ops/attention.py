@@ -36,8 +36,15 @@ class AttnWork:
     num_splits: int
 
 
+def resident_ctas(head_dim: int, decode: bool = True) -> int:
+    """CTAs per SM allowed by shared memory (Q tile + double-buffered 64-token K/V tiles)."""
+    rows = DECODE_ROWS if decode else PREFILL_ROWS
+    smem = rows * head_dim * 2 + 4 * KV_TILE * head_dim * 2
+    return max(1, (227 * 1024) // (smem + 1024))
+
+
 def build_work(q_lens: np.ndarray, seq_lens: np.ndarray, group: int, num_kv_heads: int,
-               num_sms: int = 148, max_splits: int = 16) -> AttnWork:
+               num_sms: int = 148, max_splits: int = 16, head_dim: int = 128) -> AttnWork:
     """Split the batch into CTA work items.
 
     Decode mode is used when every sequence has at most ``DECODE_ROWS`` packed rows
@@ -50,9 +57,12 @@ def build_work(q_lens: np.ndarray, seq_lens: np.ndarray, group: int, num_kv_head
         work = np.stack([np.arange(len(rows)), np.zeros(len(rows), dtype=np.int64)], 1)
         ctas = len(rows) * num_kv_heads
         max_tiles = int(math.ceil(int(np.max(seq_lens)) / KV_TILE)) if len(rows) else 1
+        # Split the KV range until the grid spans several waves of resident CTAs (decode CTAs
+        # are memory-bound; a grid of ~1 wave loses up to half the bandwidth to the tail).
+        slots = num_sms * resident_ctas(head_dim)
         splits = 1
-        while ctas * splits < 2 * num_sms and splits * 2 <= min(max_splits, max(1, max_tiles // 2)):
-            splits *= 2
+        while ctas * splits < 4 * slots and splits < max_splits and splits * 2 <= max(1, max_tiles // 2):
+            splits += 1
         return AttnWork(work.astype(np.int32), True, splits)
     seqs, starts = [], []
     for b, r in enumerate(rows):

@@ -113,15 +113,13 @@ def gemm_accumulate(x: torch.Tensor, w: torch.Tensor, acc: torch.Tensor,
     if not x.is_cuda:
         acc[:M].add_(x.float() @ w.float().t())
         return acc
-    sms = num_sms(x.device)
+    # splits=None -> stream-K: every persistent CTA gets an equal share of (tile, k-block)
+    # units, so the weight stream is balanced over all SMs whatever N and K are.
+    s = splits if splits is not None else -1
     if M <= SKINNY_MAX:
-        s = splits if splits is not None else pick_splits(N, K, sms)
         ext().gemm(w, x, acc, EPI_F32_RED_T, skinny_bn(M), s, 0, 0)
     else:
-        bn = 128
-        tiles = math.ceil(M / 128) * math.ceil(N / bn)
-        s = splits if splits is not None else (1 if tiles >= sms else max(1, min(sms // tiles, math.ceil(K / 64) // 4)))
-        ext().gemm(x, w, acc, EPI_F32_RED, bn, s, 0, 0)
+        ext().gemm(x, w, acc, EPI_F32_RED, 128, s, 0, 0)
     return acc
 
 

@@ -200,10 +200,10 @@ class ModelRunner:
         G = max(1, m.Hq // m.Hkv)
         if pad_B is not None:
             w = ops.build_work(np.ones(Bp, dtype=np.int64), np.full(Bp, self.max_model_len), G, m.Hkv, self.num_sms,
-                               max_splits=m.attn_splits_max)
+                               max_splits=m.attn_splits_max, head_dim=m.D)
         else:
             w = ops.build_work(q_lens[:Bp], sl[:Bp].astype(np.int64), G, m.Hkv, self.num_sms,
-                               max_splits=m.attn_splits_max)
+                               max_splits=m.attn_splits_max, head_dim=m.D)
         work = h[o["work"][0]:o["work"][0] + 2 * len(w.work)]
         work[:] = w.work.reshape(-1)
         self._last_work_len = len(w.work)
@@ -248,7 +248,7 @@ class ModelRunner:
             buf = torch.zeros(lay.total, dtype=torch.int32, device=self.device)
             G = max(1, m.Hq // m.Hkv)
             w = ops.build_work(np.ones(b, dtype=np.int64), np.full(b, self.max_model_len), G, m.Hkv,
-                               self.num_sms, max_splits=m.attn_splits_max)
+                               self.num_sms, max_splits=m.attn_splits_max, head_dim=m.D)
             # valid dummy metadata for the warm-up / capture runs
             h = torch.zeros(lay.total, dtype=torch.int32)
             o = lay.off
