@@ -81,6 +81,8 @@ __device__ __forceinline__ uint32_t swz(int r, int c) {
 template <int D, bool DECODE>
 __global__ void __launch_bounds__(128)
     paged_attention_kernel(const PagedAttnParams p) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int BM = DECODE ? 16 : 64;        // packed rows per CTA
   constexpr int KVW = DECODE ? 16 : kKvTile;  // tokens per warp per tile
   constexpr int CH = D / 8;                   // 16-byte chunks per row
@@ -381,6 +383,8 @@ __global__ void attn_combine_kernel(const float* __restrict__ part_o,
                                     const float* __restrict__ part_lse, __nv_bfloat16* out,
                                     long long o_stride_t, int total_tokens, int Hq,
                                     int num_splits) {
+  pdl_trigger();
+  pdl_wait();
   const int tok = blockIdx.x;
   const int head = blockIdx.y;
   float mx = -INFINITY;
@@ -414,7 +418,7 @@ static void launch_attn(const PagedAttnParams& p, int num_work, cudaStream_t str
     configured = true;
   }
   dim3 grid(num_work, p.Hkv, p.num_splits);
-  kern<<<grid, 128, smem, stream>>>(p);
+  launch_pdl(kern, grid, dim3(128), smem, stream, p);
 }
 
 void paged_attention_launch(const PagedAttnParams& p, int num_work, int head_dim, bool decode,
@@ -433,13 +437,11 @@ void paged_attention_launch(const PagedAttnParams& p, int num_work, int head_dim
   if (p.num_splits > 1) {
     dim3 grid(p.total_tokens, p.Hq);
     if (head_dim == 128)
-      attn_combine_kernel<128><<<grid, 128, 0, stream>>>(p.part_o, p.part_lse, p.out,
-                                                         p.o_stride_t, p.total_tokens, p.Hq,
-                                                         p.num_splits);
+      launch_pdl(attn_combine_kernel<128>, grid, dim3(128), 0, stream, (const float*)p.part_o,
+                 (const float*)p.part_lse, p.out, p.o_stride_t, p.total_tokens, p.Hq, p.num_splits);
     else
-      attn_combine_kernel<64><<<grid, 64, 0, stream>>>(p.part_o, p.part_lse, p.out,
-                                                       p.o_stride_t, p.total_tokens, p.Hq,
-                                                       p.num_splits);
+      launch_pdl(attn_combine_kernel<64>, grid, dim3(64), 0, stream, (const float*)p.part_o,
+                 (const float*)p.part_lse, p.out, p.o_stride_t, p.total_tokens, p.Hq, p.num_splits);
   }
 }
 

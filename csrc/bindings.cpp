@@ -215,20 +215,22 @@ void silu_mul(at::Tensor& inp, at::Tensor& out, int64_t blk, bool clear_input, i
 }
 
 void embedding(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out,
-               int64_t vocab_start, int64_t vocab_end) {
+               int64_t vocab_start, int64_t vocab_end, c10::optional<at::Tensor> last_tok) {
   CHECK_CUDA(ids);
   TORCH_CHECK(ids.scalar_type() == at::kInt, "ids must be int32");
   const c10::cuda::CUDAGuard guard(ids.device());
   b200::embedding_launch(ids.data_ptr<int>(), reinterpret_cast<const __nv_bfloat16*>(table.data_ptr()),
                          reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), (int)ids.size(0),
-                         (int)table.size(1), (int)vocab_start, (int)vocab_end, cur_stream());
+                         (int)table.size(1), (int)vocab_start, (int)vocab_end,
+                         last_tok.has_value() ? last_tok->data_ptr<int>() : nullptr, cur_stream());
   check_launch("embedding");
 }
 
 void sample(const at::Tensor& logits, const at::Tensor& temperature, const at::Tensor& top_k,
             const at::Tensor& top_p, c10::optional<at::Tensor> min_p, const at::Tensor& seeds,
             const at::Tensor& offsets, at::Tensor& out_tokens,
-            c10::optional<at::Tensor> out_logprob, int64_t vocab_offset) {
+            c10::optional<at::Tensor> out_logprob, int64_t vocab_offset,
+            c10::optional<at::Tensor> row_slots, c10::optional<at::Tensor> last_tok) {
   CHECK_CUDA(logits);
   const c10::cuda::CUDAGuard guard(logits.device());
   b200::SampleParams p{};
@@ -246,6 +248,11 @@ void sample(const at::Tensor& logits, const at::Tensor& temperature, const at::T
   p.out_tokens = out_tokens.data_ptr<int>();
   p.out_logprob = out_logprob.has_value() ? out_logprob->data_ptr<float>() : nullptr;
   p.vocab_offset = (int)vocab_offset;
+  if (row_slots.has_value()) {
+    TORCH_CHECK(last_tok.has_value(), "row_slots needs last_tok");
+    p.row_slots = row_slots->data_ptr<int>();
+    p.last_tok = last_tok->data_ptr<int>();
+  }
   b200::sample_launch(p, cur_stream());
   check_launch("sample");
 }

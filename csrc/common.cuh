@@ -12,6 +12,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #ifndef B200_WAIT_TIMEOUT_NS
 #define B200_WAIT_TIMEOUT_NS 2000000000ull  // 2 s: far above any legitimate wait
 #endif
@@ -56,6 +58,20 @@ __device__ __forceinline__ bool elect_one() {
       "{\n\t.reg .pred P;\n\telect.sync _|P, 0xffffffff;\n\tselp.u32 %0, 1, 0, P;\n\t}"
       : "=r"(pred));
   return pred != 0;
+}
+
+// ----------------------------------------------------------------------------------------
+// Programmatic dependent launch.  Kernels are launched with programmatic stream
+// serialization (launch_pdl below): a kernel may start while its predecessor finishes, does
+// its prologue, and must call pdl_wait() before it reads anything the predecessor wrote or
+// writes anything the predecessor may still read.  pdl_trigger() lets the successor launch.
+// Both are no-ops when the kernel was launched without the attribute.
+// ----------------------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 // ----------------------------------------------------------------------------------------
@@ -311,5 +327,24 @@ __device__ __forceinline__ T warp_max(T v) {
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
   return v;
 }
+
+#ifndef __CUDACC_RTC__
+// Launch with programmatic stream serialization (see pdl_wait / pdl_trigger).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+#endif
 
 }  // namespace b200

@@ -157,29 +157,69 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 0) {
     // ------------------------------ TMA producer ------------------------------
     if (elect_one()) {
-      const uint64_t hint_a = (EPI == EPI_BF16_T || EPI == EPI_F32_RED_T)
-                                  ? policy_evict_first()  // A = weights, streamed once
-                                  : policy_evict_last();
-      const uint64_t hint_b = (EPI == EPI_BF16_T || EPI == EPI_F32_RED_T)
-                                  ? policy_evict_last()   // B = activations, reused
-                                  : policy_evict_first();
+      constexpr bool kWeightIsA = (EPI == EPI_BF16_T || EPI == EPI_F32_RED_T);
+      const uint64_t hint_a = kWeightIsA ? policy_evict_first()  // A = weights, streamed once
+                                         : policy_evict_last();
+      const uint64_t hint_b = kWeightIsA ? policy_evict_last()   // B = activations, reused
+                                         : policy_evict_first();
+      auto load_a = [&](int s, int kb, int mb) {
+        tma_load_2d(&tmA, &full_bar[s], smA + s * kATileBytes, kb * kBK, mb * kBM, hint_a);
+      };
+      auto load_b = [&](int s, int kb, int nb) {
+        tma_load_2d(&tmB, &full_bar[s], smB + s * kBTileBytes, kb * kBK, nb * BN, hint_b);
+      };
       uint32_t it = 0;
       bool ok = true;
       SegCursor cur(p);
-      int mb, nb, k0, k1;
-      while (ok && cur.next(p, mb, nb, k0, k1)) {
-        for (int kb = k0; kb < k1; ++kb, ++it) {
-          const int s = it % STAGES;
-          const uint32_t ph = (it / STAGES) & 1;
-          if (!mbar_wait_abortable(&empty_bar[s], ph ^ 1, kTimeoutSmemEmpty, p.status, abort_flag)) {
-            ok = false;
-            break;
+      int mb = 0, nb = 0, k0 = 0, k1 = 0;
+      bool have = cur.next(p, mb, nb, k0, k1);
+      int kb = k0;
+      // Phase 1: the weight operand of the first STAGES k-blocks does not depend on the
+      // previous kernel, so it streams in before the dependency wait.
+      int pre_mb[STAGES], pre_nb[STAGES], pre_kb[STAGES];
+      int npre = 0;
+#pragma unroll
+      for (int i = 0; i < STAGES; ++i) {
+        if (have) {
+          mbar_arrive_expect_tx(&full_bar[i], kStageBytes);
+          if (kWeightIsA) load_a(i, kb, mb); else load_b(i, kb, nb);
+          pre_mb[i] = mb;
+          pre_nb[i] = nb;
+          pre_kb[i] = kb;
+          npre = i + 1;
+          ++it;
+          if (++kb == k1) {
+            have = cur.next(p, mb, nb, k0, k1);
+            kb = k0;
           }
-          mbar_arrive_expect_tx(&full_bar[s], kStageBytes);
-          tma_load_2d(&tmA, &full_bar[s], smA + s * kATileBytes, kb * kBK, mb * kBM, hint_a);
-          tma_load_2d(&tmB, &full_bar[s], smB + s * kBTileBytes, kb * kBK, nb * BN, hint_b);
         }
       }
+      pdl_wait();
+#pragma unroll
+      for (int i = 0; i < STAGES; ++i) {
+        if (i < npre) {
+          if (kWeightIsA) load_b(i, pre_kb[i], pre_nb[i]); else load_a(i, pre_kb[i], pre_mb[i]);
+        }
+      }
+      // Phase 2: steady state.
+      while (have) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        if (!mbar_wait_abortable(&empty_bar[s], ph ^ 1, kTimeoutSmemEmpty, p.status, abort_flag)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&full_bar[s], kStageBytes);
+        load_a(s, kb, mb);
+        load_b(s, kb, nb);
+        ++it;
+        if (++kb == k1) {
+          have = cur.next(p, mb, nb, k0, k1);
+          kb = k0;
+        }
+      }
+      // The successor may launch once every CTA has issued its last load.
+      pdl_trigger();
       if (!ok) {
         // Drain the copies still in flight before the CTA's shared memory is released.
         const uint32_t first = it > (uint32_t)STAGES ? it - STAGES : 0;
@@ -227,6 +267,7 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     // ------------------------------ epilogue ------------------------------
+    pdl_wait();  // outputs may still be read (or, for reductions, cleared) by the predecessor
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int row = q * 32 + lane;
     int t_local = 0;
@@ -394,7 +435,7 @@ static void launch_impl(const CUtensorMap& ta, const CUtensorMap& tb, const Gemm
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     configured = true;
   }
-  kern<<<grid, 192, smem, stream>>>(ta, tb, p);
+  launch_pdl(kern, dim3(grid), dim3(192), smem, stream, ta, tb, p);
 }
 
 int num_sms_cached() {

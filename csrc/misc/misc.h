@@ -35,8 +35,11 @@ void silu_mul_launch(void* in, bool in_is_f32, long long in_stride, __nv_bfloat1
                      long long out_stride, int T, int I, int blk, bool clear_input, int act,
                      float limit, float alpha, cudaStream_t stream);
 
+// ids < 0 are device-resident tokens: id = last_tok[-id - 1] (the token a previous step
+// sampled into that request slot; see SampleParams::row_slots).
 void embedding_launch(const int* ids, const __nv_bfloat16* table, __nv_bfloat16* out, int T,
-                      int H, int vocab_start, int vocab_end, cudaStream_t stream);
+                      int H, int vocab_start, int vocab_end, const int* last_tok,
+                      cudaStream_t stream);
 
 struct SampleParams {
   const void* logits;          // [B, V] (bf16 or fp32)
@@ -53,6 +56,8 @@ struct SampleParams {
   float* out_logprob;          // [B] log-probability of the sampled token (may be null)
   int vocab_offset;            // added to the sampled index (vocab shard start)
   float* out_max;              // [B] optional: row max of the processed logits (sharded merge)
+  const int* row_slots;        // [B] optional: request slot of each row ...
+  int* last_tok;               // ... whose device-resident last token is updated
 };
 void sample_launch(const SampleParams& p, cudaStream_t stream);
 

@@ -99,6 +99,8 @@ __global__ void __launch_bounds__(256) add_rmsnorm_kernel(TX* x, long long x_str
                                                           const __nv_bfloat16* __restrict__ w,
                                                           __nv_bfloat16* out, long long o_stride,
                                                           int H, float eps, bool clear_x) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float red[32];
   const long long row = blockIdx.x;
   TX* xr = x + row * x_stride;
@@ -149,9 +151,8 @@ static void launch_norm(TX* x, long long xs, __nv_bfloat16* res, long long rs,
   const int nv = (vecs + threads - 1) / threads;
 #define B200_NORM(NV_)                                                                   \
   if (nv <= NV_) {                                                                       \
-    add_rmsnorm_kernel<TX, HAS_RES, NV_><<<rows, threads, 0, stream>>>(x, xs, res, rs, w, \
-                                                                         out, os, H, eps, \
-                                                                         clear);          \
+    launch_pdl(add_rmsnorm_kernel<TX, HAS_RES, NV_>, dim3(rows), dim3(threads), 0, stream, \
+               x, xs, res, rs, w, out, os, H, eps, clear);                                 \
     return;                                                                              \
   }
   B200_NORM(1)
@@ -192,6 +193,8 @@ void add_rmsnorm_launch(void* x, bool x_is_f32, long long x_stride, __nv_bfloat1
 // ------------------------------------------------------------------------------------------
 template <typename TIN, int D>
 __global__ void __launch_bounds__(256) rope_kv_write_kernel(const RopeKvParams p, TIN* qkv) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int PER = D / 32;  // elements per lane: lane l owns l, l + 32, l + 64, ...
   const int t = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -289,9 +292,11 @@ void rope_kv_write_launch(const RopeKvParams& p, void* qkv, bool qkv_is_f32, int
 #define B200_ROPE(D_)                                                                       \
   if (p.head_dim == D_) {                                                                   \
     if (qkv_is_f32)                                                                         \
-      rope_kv_write_kernel<float, D_><<<T, 256, 0, stream>>>(p, (float*)qkv);               \
+      launch_pdl(rope_kv_write_kernel<float, D_>, dim3(T), dim3(256), 0, stream, p,          \
+                 (float*)qkv);                                                              \
     else                                                                                    \
-      rope_kv_write_kernel<__nv_bfloat16, D_><<<T, 256, 0, stream>>>(p, (__nv_bfloat16*)qkv); \
+      launch_pdl(rope_kv_write_kernel<__nv_bfloat16, D_>, dim3(T), dim3(256), 0, stream, p,  \
+                 (__nv_bfloat16*)qkv);                                                      \
     return;                                                                                 \
   }
   B200_ROPE(64)
@@ -308,6 +313,8 @@ template <typename TIN, int VEC>
 __global__ void silu_mul_kernel(TIN* in, long long in_stride, __nv_bfloat16* out,
                                 long long out_stride, int I, int blk, bool clear_input,
                                 float limit, float alpha, int act) {
+  pdl_trigger();
+  pdl_wait();
   const long long t = blockIdx.y;
   TIN* r = in + t * in_stride;
   const int j = (blockIdx.x * blockDim.x + threadIdx.x) * VEC;
@@ -369,18 +376,18 @@ void silu_mul_launch(void* in, bool in_is_f32, long long in_stride, __nv_bfloat1
   if (vec8) {
     dim3 grid((I / 8 + 127) / 128, T);
     if (in_is_f32)
-      silu_mul_kernel<float, 8><<<grid, 128, 0, stream>>>((float*)in, in_stride, out, out_stride, I,
+      launch_pdl(silu_mul_kernel<float, 8>, grid, dim3(128), 0, stream, (float*)in, in_stride, out, out_stride, I,
                                                           blk, clear_input, limit, alpha, act);
     else
-      silu_mul_kernel<__nv_bfloat16, 8><<<grid, 128, 0, stream>>>(
+      launch_pdl(silu_mul_kernel<__nv_bfloat16, 8>, grid, dim3(128), 0, stream, 
           (__nv_bfloat16*)in, in_stride, out, out_stride, I, blk, false, limit, alpha, act);
   } else {
     dim3 grid((I + 255) / 256, T);
     if (in_is_f32)
-      silu_mul_kernel<float, 1><<<grid, 256, 0, stream>>>((float*)in, in_stride, out, out_stride, I,
+      launch_pdl(silu_mul_kernel<float, 1>, grid, dim3(256), 0, stream, (float*)in, in_stride, out, out_stride, I,
                                                           blk, clear_input, limit, alpha, act);
     else
-      silu_mul_kernel<__nv_bfloat16, 1><<<grid, 256, 0, stream>>>(
+      launch_pdl(silu_mul_kernel<__nv_bfloat16, 1>, grid, dim3(256), 0, stream, 
           (__nv_bfloat16*)in, in_stride, out, out_stride, I, blk, false, limit, alpha, act);
   }
 }
@@ -389,9 +396,13 @@ void silu_mul_launch(void* in, bool in_is_f32, long long in_stride, __nv_bfloat1
 // Embedding lookup (vocab-sharded).
 // ------------------------------------------------------------------------------------------
 __global__ void embedding_kernel(const int* __restrict__ ids, const __nv_bfloat16* __restrict__ table,
-                                 __nv_bfloat16* out, int H, int vocab_start, int vocab_end) {
+                                 __nv_bfloat16* out, int H, int vocab_start, int vocab_end,
+                                 const int* __restrict__ last_tok) {
+  pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.x;
-  const int id = ids[t];
+  int id = ids[t];
+  if (id < 0 && last_tok != nullptr) id = last_tok[-id - 1];
   const bool own = id >= vocab_start && id < vocab_end;
   const uint4* src = reinterpret_cast<const uint4*>(table + (long long)(own ? id - vocab_start : 0) * H);
   uint4* dst = reinterpret_cast<uint4*>(out + (long long)t * H);
@@ -399,10 +410,12 @@ __global__ void embedding_kernel(const int* __restrict__ ids, const __nv_bfloat1
 }
 
 void embedding_launch(const int* ids, const __nv_bfloat16* table, __nv_bfloat16* out, int T,
-                      int H, int vocab_start, int vocab_end, cudaStream_t stream) {
+                      int H, int vocab_start, int vocab_end, const int* last_tok,
+                      cudaStream_t stream) {
   if (T == 0) return;
   if (H % 8 != 0) throw std::invalid_argument("embedding: hidden size must be a multiple of 8");
-  embedding_kernel<<<T, 128, 0, stream>>>(ids, table, out, H, vocab_start, vocab_end);
+  launch_pdl(embedding_kernel, dim3(T), dim3(128), 0, stream, ids, table, out, H, vocab_start,
+             vocab_end, last_tok);
 }
 
 }  // namespace b200

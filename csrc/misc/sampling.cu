@@ -175,6 +175,8 @@ __device__ uint32_t radix_select(const void* row, bool f32, int V, float inv_t, 
 }  // namespace
 
 __global__ void __launch_bounds__(kThreads) sample_kernel(const SampleParams p) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ ArgMax red_am[32];
   __shared__ float red[32];
   __shared__ float hist[256];
@@ -207,6 +209,7 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(const SampleParams p) 
     }
     if (threadIdx.x == 0) {
       p.out_tokens[b] = best.i + p.vocab_offset;
+      if (p.row_slots) p.last_tok[p.row_slots[b]] = best.i + p.vocab_offset;
       if (p.out_max) p.out_max[b] = m;
     }
     return;
@@ -248,6 +251,7 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(const SampleParams p) 
   if (threadIdx.x == 0) {
     const int tok = g.i == 0x7fffffff ? best.i : g.i;
     p.out_tokens[b] = tok + p.vocab_offset;
+    if (p.row_slots) p.last_tok[p.row_slots[b]] = tok + p.vocab_offset;
     if (p.out_logprob) p.out_logprob[b] = load_logit(row, p.logits_f32, tok) * inv_t - m - logf(z);
     if (p.out_max) p.out_max[b] = m;
   }
@@ -255,12 +259,14 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(const SampleParams p) 
 
 void sample_launch(const SampleParams& p, cudaStream_t stream) {
   if (p.B == 0) return;
-  sample_kernel<<<p.B, kThreads, 0, stream>>>(p);
+  launch_pdl(sample_kernel, dim3(p.B), dim3(kThreads), 0, stream, p);
 }
 
 __global__ void __launch_bounds__(kThreads)
     argmax_kernel(const void* logits, bool f32, long long stride, int V, int* out_idx,
                   float* out_val, int vocab_offset) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ ArgMax red_am[32];
   const int b = blockIdx.x;
   const void* row = f32 ? (const void*)(reinterpret_cast<const float*>(logits) + b * stride)
@@ -278,8 +284,8 @@ __global__ void __launch_bounds__(kThreads)
 void argmax_launch(const void* logits, bool f32, long long stride, int B, int V, int* out_idx,
                    float* out_val, int vocab_offset, cudaStream_t stream) {
   if (B == 0) return;
-  argmax_kernel<<<B, kThreads, 0, stream>>>(logits, f32, stride, V, out_idx, out_val,
-                                            vocab_offset);
+  launch_pdl(argmax_kernel, dim3(B), dim3(kThreads), 0, stream, logits, f32, stride, V, out_idx,
+             out_val, vocab_offset);
 }
 
 }  // namespace b200

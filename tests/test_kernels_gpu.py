@@ -239,3 +239,21 @@ def test_sampling_topk_topp_support(cuda_device):
     offs = torch.full((B,), 7, dtype=torch.int32, device=cuda_device)
     assert torch.equal(ops.sample(logits, temp, tk, tp, seeds, offs),
                        ops.sample(logits, temp, tk, tp, seeds, offs))
+
+
+def test_device_resident_tokens(cuda_device):
+    """Negative ids read the request slot's last sampled token; the sampler writes slots."""
+    V, H = 1000, 256
+    table = torch.randn(V, H, device=cuda_device, dtype=torch.bfloat16)
+    last = torch.zeros(8, dtype=torch.int32, device=cuda_device)
+    logits = torch.randn(3, V, device=cuda_device)
+    z = torch.zeros(3, device=cuda_device)
+    tk = torch.zeros(3, dtype=torch.int32, device=cuda_device)
+    tp = torch.ones(3, device=cuda_device)
+    sd = torch.zeros(3, dtype=torch.int64, device=cuda_device)
+    slots = torch.tensor([5, 2, 7], dtype=torch.int32, device=cuda_device)
+    tok = ops.sample(logits, z, tk, tp, sd, tk, row_slots=slots, last_tok=last)
+    assert torch.equal(last[slots.long()], tok)
+    ids = torch.tensor([-(5 + 1), 17, -(7 + 1)], dtype=torch.int32, device=cuda_device)
+    out = ops.embedding(ids, table, last_tok=last)
+    assert torch.equal(out[0], table[tok[0]]) and torch.equal(out[1], table[17]) and torch.equal(out[2], table[tok[2]])

@@ -55,3 +55,23 @@ def test_preemption_under_block_pressure():
     tight = LLM(d, device="cpu", max_num_seqs=8, max_model_len=128, num_gpu_blocks=14)
     outs = tight.generate(prompts, sp)
     assert [o.outputs[0].token_ids for o in outs] == [o.outputs[0].token_ids for o in ref]
+
+
+def test_async_scheduling_matches_sync():
+    """Asynchronous scheduling (step N+1 launched before step N's tokens are processed; decode
+    inputs read from the device-resident token slots) yields the same tokens, including when a
+    stop token ends a request while its next step is already in flight."""
+    d, hf = tiny_llama_checkpoint()
+    prompts = random_prompts(n=5, length=24, seed=7)
+    kw = dict(device="cpu", max_num_seqs=4, max_model_len=128, num_gpu_blocks=64, max_num_batched_tokens=40)
+    sync = LLM(d, async_scheduling=False, **kw)
+    base = sync.generate(prompts, SamplingParams(temperature=0, max_tokens=12, ignore_eos=True))
+    stop_tok = base[1].outputs[0].token_ids[4]
+    sps = [SamplingParams(temperature=0, max_tokens=12, ignore_eos=True)] * 5
+    sps[1] = SamplingParams(temperature=0, max_tokens=12, stop_token_ids=[stop_tok])
+    ref = sync.generate(prompts, sps)
+    asy = LLM(d, async_scheduling=True, **kw)
+    got = asy.generate(prompts, sps)
+    assert [o.outputs[0].token_ids for o in got] == [o.outputs[0].token_ids for o in ref]
+    assert got[1].outputs[0].finish_reason == "stop"
+    assert len(asy.engine._free_slots) == asy.engine.runner.max_slots - 1

@@ -38,6 +38,7 @@ class EngineArgs:
     dtype: str = "bfloat16"
     device: str = "cuda"
     cuda_graphs: bool = True
+    async_scheduling: bool | None = None  # default: on for CUDA devices
     additional_config: dict = field(default_factory=dict)
 
 
@@ -113,6 +114,10 @@ class LLMEngine:
         if isinstance(self.eos_token_id, list):
             self.eos_token_id = self.eos_token_id[0] if self.eos_token_id else None
         self.num_steps = 0
+        self.async_scheduling = (self.device.type == "cuda" if args.async_scheduling is None
+                                 else bool(args.async_scheduling))
+        self._inflight = None  # (SchedulerOutput, StepHandle) of the launched, unprocessed step
+        self._free_slots = list(range(self.runner.max_slots - 2, -1, -1))
 
     # ---------------------------------------------------------------- requests
     def add_request(self, prompt_token_ids: list[int], params: SamplingParams | None = None,
@@ -122,31 +127,68 @@ class LLMEngine:
         req = Request(rid, list(prompt_token_ids), params, eos_token_id=self.eos_token_id)
         if arrival_time is not None:
             req.arrival_time = arrival_time
-        self.scheduler.add_request(req)
+        if not self._free_slots:
+            raise RuntimeError("too many unfinished requests for the device token slots")
+        req.slot = self._free_slots.pop()
+        try:
+            self.scheduler.add_request(req)
+        except Exception:
+            self._free_slots.append(req.slot)
+            raise
         return rid
 
     def abort_request(self, request_id: str):
+        req = self.scheduler.requests.get(request_id)
         self.scheduler.abort_request(request_id)
+        if req is not None and req.num_pending == 0 and req.slot >= 0:
+            self._free_slots.append(req.slot)
+            req.slot = -1
 
     def has_unfinished_requests(self) -> bool:
-        return self.scheduler.has_unfinished()
+        return self.scheduler.has_unfinished() or self._inflight is not None
 
     # ---------------------------------------------------------------- stepping
-    def step(self) -> list[Request]:
-        out = self.scheduler.schedule()
-        if out.empty:
-            return []
-        want_lp = any(s.req.sampling_params.logprobs for s in out.scheduled if s.samples)
-        toks, lps = self.runner.execute(out, want_logprobs=want_lp)
+    def _process(self, out, handle) -> list[Request]:
+        toks, lps = handle.result()
         now = time.perf_counter()
         finished = self.scheduler.update(out, toks, lps, now=now)
-        self.num_steps += 1
-        self.metrics.steps += 1
+        for req in finished:
+            if req.slot >= 0 and req.num_pending == 0:
+                self._free_slots.append(req.slot)
+                req.slot = -1
+        # requests that stopped earlier and just received their last in-flight token
+        for s in out.scheduled:
+            r = s.req
+            if r.status.finished and r.num_pending == 0 and r.slot >= 0:
+                self._free_slots.append(r.slot)
+                r.slot = -1
+        return finished
+
+    def step(self) -> list[Request]:
+        """Schedule and launch the next step; with asynchronous scheduling the results of the
+        previous step are processed while this one runs on the GPU."""
+        out = self.scheduler.schedule()
+        handle = None
+        if not out.empty:
+            want_lp = any(s.req.sampling_params.logprobs for s in out.scheduled if s.samples)
+            handle = self.runner.launch(out, want_logprobs=want_lp)
+            self.num_steps += 1
+            self.metrics.steps += 1
+        finished = []
+        if not self.async_scheduling:
+            if handle is not None:
+                finished = self._process(out, handle)
+            return finished
+        if self._inflight is not None:
+            finished = self._process(*self._inflight)
+            self._inflight = None
+        if handle is not None:
+            self._inflight = (out, handle)
         return finished
 
     def run_until_done(self) -> list[Request]:
         done = []
-        while self.scheduler.has_unfinished():
+        while self.scheduler.has_unfinished() or self._inflight is not None:
             done.extend(self.step())
         return done
 

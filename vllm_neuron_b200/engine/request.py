@@ -34,6 +34,8 @@ class Request:
     status: RequestStatus = RequestStatus.WAITING
     num_computed_tokens: int = 0
     num_cached_tokens: int = 0  # prefix-cache hits of the current admission
+    num_pending: int = 0        # tokens sampled by launched steps whose results are not back yet
+    slot: int = -1              # device slot holding this request's last sampled token
     block_ids: list[int] = field(default_factory=list)
     first_token_time: float | None = None
     finish_time: float | None = None
@@ -46,7 +48,13 @@ class Request:
 
     @property
     def num_tokens(self) -> int:
+        """Tokens known on the host (prompt + received outputs)."""
         return len(self.prompt_token_ids) + len(self.output_token_ids)
+
+    @property
+    def num_tokens_scheduled(self) -> int:
+        """Tokens including those still being sampled by in-flight steps."""
+        return len(self.prompt_token_ids) + len(self.output_token_ids) + self.num_pending
 
     def token_at(self, i: int) -> int:
         n = len(self.prompt_token_ids)

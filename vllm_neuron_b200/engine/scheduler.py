@@ -111,8 +111,9 @@ class Scheduler:
         i = 0
         while i < len(self.running) and budget > 0:
             req = self.running[i]
-            n = req.num_tokens - req.num_computed_tokens
-            if n <= 0:
+            n = req.num_tokens_scheduled - req.num_computed_tokens
+            if n <= 0 or len(req.output_token_ids) + req.num_pending >= req.max_tokens:
+                # nothing to compute, or its last token is already being sampled
                 i += 1
                 continue
             is_prefill = n > 1 or req.num_computed_tokens < req.num_prompt_tokens
@@ -121,7 +122,7 @@ class Scheduler:
                 i += 1
                 continue
             n = min(n, budget)
-            if n < req.num_tokens - req.num_computed_tokens and not self.enable_chunked_prefill:
+            if n < req.num_tokens_scheduled - req.num_computed_tokens and not self.enable_chunked_prefill:
                 i += 1
                 continue
             ok = True
@@ -134,7 +135,7 @@ class Scheduler:
             if not ok:
                 break
             out.scheduled.append(ScheduledRequest(req, req.num_computed_tokens, n,
-                                                  req.num_computed_tokens + n >= req.num_tokens))
+                                                  req.num_computed_tokens + n >= req.num_tokens_scheduled))
             scheduled_ids.add(req.request_id)
             budget -= n
             has_prefill |= is_prefill
@@ -145,6 +146,8 @@ class Scheduler:
                 if not self.mixed_batches and (has_decode or has_prefill):
                     break
                 req = self.waiting[0]
+                if req.num_pending:
+                    break  # a preempted request whose last token is still in flight
                 if not req.block_ids:
                     cached = self.bm.match_prefix(req)
                     req.num_computed_tokens = cached
@@ -163,9 +166,15 @@ class Scheduler:
                 req.status = RequestStatus.RUNNING
                 self.running.append(req)
                 out.scheduled.append(ScheduledRequest(req, req.num_computed_tokens, n,
-                                                      req.num_computed_tokens + n >= req.num_tokens))
+                                                      req.num_computed_tokens + n >= req.num_tokens_scheduled))
                 budget -= n
                 has_prefill = True
+        # The KV of scheduled tokens is written by this step, and sampling rows add a
+        # placeholder token until their result comes back (asynchronous scheduling).
+        for sr in out.scheduled:
+            sr.req.num_computed_tokens = sr.start + sr.num_tokens
+            if sr.samples:
+                sr.req.num_pending += 1
         out.num_tokens = sum(s.num_tokens for s in out.scheduled)
         out.padded_tokens = bucket_for(self.tok_buckets, out.num_tokens)
         out.padded_seqs = bucket_for(self.seq_buckets, len(out.scheduled))
@@ -181,15 +190,20 @@ class Scheduler:
         k = 0
         for s in out.scheduled:
             req = s.req
-            req.num_computed_tokens = s.start + s.num_tokens
-            self.bm.commit_full_blocks(req)
             if not s.samples:
+                if not req.status.finished:
+                    self.bm.commit_full_blocks(req)
                 continue
             tok = int(sampled[k])
-            if logprobs is not None:
-                req.output_logprobs.append(float(logprobs[k]))
+            lp = float(logprobs[k]) if logprobs is not None else None
             k += 1
+            req.num_pending -= 1
+            if req.status.finished:
+                continue  # stopped by an earlier token; this one was computed speculatively
+            if lp is not None:
+                req.output_logprobs.append(lp)
             req.output_token_ids.append(tok)
+            self.bm.commit_full_blocks(req)
             if now is not None:
                 if req.first_token_time is None:
                     req.first_token_time = now

@@ -51,6 +51,7 @@ class ForwardBatch:
     decode: bool
     num_splits: int
     num_tokens: int
+    last_tok: torch.Tensor | None = None  # device-resident tokens for ids < 0
 
 
 def _shard(n: int, world: int, rank: int) -> tuple[int, int]:
@@ -170,7 +171,8 @@ class LlamaForCausalLM(torch.nn.Module):
         tp = self.tp
         res = self.ws_residual[:T]
         x = self.ws_x[:T]
-        ops.embedding(b.input_ids, self.embed, self.vocab_start, self.vocab_start + self.V_local, out=res)
+        ops.embedding(b.input_ids, self.embed, self.vocab_start, self.vocab_start + self.V_local, out=res,
+                      last_tok=b.last_tok)
         tp.all_reduce_(res)
         ops.rmsnorm(res, self.layers[0].input_norm, self.eps, out=x)
         nL = len(self.layers)

@@ -113,9 +113,15 @@ def gemm_accumulate(x: torch.Tensor, w: torch.Tensor, acc: torch.Tensor,
     if not x.is_cuda:
         acc[:M].add_(x.float() @ w.float().t())
         return acc
-    # splits=None -> stream-K: every persistent CTA gets an equal share of (tile, k-block)
-    # units, so the weight stream is balanced over all SMs whatever N and K are.
-    s = splits if splits is not None else -1
+    # splits=None: split-K when the row tiles alone under-fill the SMs (measured faster for
+    # the small qkv / o projections), stream-K (-1: every persistent CTA takes an equal share
+    # of (tile, k-block) units) when there are more tiles than SMs.
+    if splits is None:
+        rows = N if M <= SKINNY_MAX else math.ceil(M / 128) * 128 * math.ceil(N / 128)
+        tiles = math.ceil(rows / 128)
+        s = pick_splits(rows, K, num_sms(x.device)) if tiles < num_sms(x.device) else -1
+    else:
+        s = splits
     if M <= SKINNY_MAX:
         ext().gemm(w, x, acc, EPI_F32_RED_T, skinny_bn(M), s, 0, 0)
     else:

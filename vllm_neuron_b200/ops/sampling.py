@@ -14,15 +14,20 @@ from ._ext import ext
 def sample(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor,
            top_p: torch.Tensor, seeds: torch.Tensor, offsets: torch.Tensor,
            min_p: torch.Tensor | None = None, out: torch.Tensor | None = None,
-           out_logprob: torch.Tensor | None = None, vocab_offset: int = 0) -> torch.Tensor:
+           out_logprob: torch.Tensor | None = None, vocab_offset: int = 0,
+           row_slots: torch.Tensor | None = None, last_tok: torch.Tensor | None = None) -> torch.Tensor:
+    """Sample one token per row.  With ``row_slots``, each row's token is also stored in
+    ``last_tok[row_slots[row]]`` (the device-resident input of that request's next step)."""
     B = logits.shape[0]
     if out is None:
         out = torch.empty((B,), dtype=torch.int32, device=logits.device)
     if not logits.is_cuda:
         out.copy_(sample_ref(logits, temperature, top_k, top_p, seeds, offsets, min_p) + vocab_offset)
+        if row_slots is not None:
+            last_tok[row_slots.long()] = out
         return out
     ext().sample(logits, temperature, top_k, top_p, min_p, seeds, offsets, out, out_logprob,
-                 vocab_offset)
+                 vocab_offset, row_slots, last_tok)
     return out
 
 

@@ -47,7 +47,8 @@ class Layout:
         for name, n in (("ids", self.T), ("pos", self.T), ("slot", self.T), ("qstart", self.B + 1),
                         ("seqlen", self.B), ("lidx", self.S), ("work", 2 * self.W),
                         ("bt", self.B * self.nblk), ("temp", self.S), ("topk", self.S),
-                        ("topp", self.S), ("minp", self.S), ("seed", 2 * self.S), ("offs", self.S)):
+                        ("topp", self.S), ("minp", self.S), ("seed", 2 * self.S), ("offs", self.S),
+                        ("rslot", self.S)):
             self.off[name] = (o, n)
             o += _round(n)
         self.total = o
@@ -76,11 +77,20 @@ class ModelRunner:
         self.num_sms = torch.cuda.get_device_properties(self.device).multi_processor_count if self.is_cuda else 148
         max_layout = Layout(self.max_tokens, max_num_seqs, max_num_seqs, self._max_work(), self.max_blocks)
         pin = self.is_cuda
-        self.host_buf = torch.zeros(max_layout.total, dtype=torch.int32, pin_memory=pin)
-        self.dev_buf = torch.zeros(max_layout.total, dtype=torch.int32, device=self.device)
+        # Two pinned input buffers and two pinned output buffers: with asynchronous
+        # scheduling, step N+1 is packed while step N's copies may still be in flight.
+        self.host_bufs = [torch.zeros(max_layout.total, dtype=torch.int32, pin_memory=pin) for _ in range(2)]
+        self.host_buf = self.host_bufs[0]
         self.host_np = self.host_buf.numpy()
-        self.tok_host = torch.zeros(max_num_seqs, dtype=torch.int32, pin_memory=pin)
-        self.lp_host = torch.zeros(max_num_seqs, dtype=torch.float32, pin_memory=pin)
+        self._buf_idx = 0
+        self.dev_buf = torch.zeros(max_layout.total, dtype=torch.int32, device=self.device)
+        self.tok_hosts = [torch.zeros(max_num_seqs, dtype=torch.int32, pin_memory=pin) for _ in range(2)]
+        self.lp_hosts = [torch.zeros(max_num_seqs, dtype=torch.float32, pin_memory=pin) for _ in range(2)]
+        self.tok_host, self.lp_host = self.tok_hosts[0], self.lp_hosts[0]
+        # Device-resident last sampled token of every request slot (async decode inputs).
+        self.max_slots = 2 * max_num_seqs + 8
+        self.pad_slot = self.max_slots - 1
+        self.last_tok = torch.zeros(self.max_slots, dtype=torch.int32, device=self.device)
         self.tok_dev = torch.zeros(max_num_seqs, dtype=torch.int32, device=self.device)
         self.lp_dev = torch.zeros(max_num_seqs, dtype=torch.float32, device=self.device)
         self.h2d_bytes = 0
@@ -146,12 +156,21 @@ class ModelRunner:
         minp = h[o["minp"][0]:o["minp"][0] + lay.S].view(np.float32)
         seed = h[o["seed"][0]:o["seed"][0] + 2 * lay.S].view(np.int64)
         offs = h[o["offs"][0]:o["offs"][0] + lay.S]
+        rslot = h[o["rslot"][0]:o["rslot"][0] + lay.S]
         for i, sr in enumerate(sch):
             req = sr.req
             n = sr.num_tokens
             st = sr.start
             P = req.num_prompt_tokens
-            if st >= P:
+            known = P + len(req.output_token_ids)
+            if st + n > known:
+                # the last input token was sampled by a step still in flight: it is read on
+                # the device from the request's slot (id = -(slot + 1))
+                nk = max(0, known - st)
+                if nk:
+                    ids[t:t + nk] = (req.prompt_token_ids + req.output_token_ids)[st:st + nk]
+                ids[t + nk:t + n] = -(req.slot + 1)
+            elif st >= P:
                 ids[t:t + n] = req.output_token_ids[st - P:st - P + n]
             elif st + n <= P:
                 ids[t:t + n] = req.prompt_token_ids[st:st + n]
@@ -176,7 +195,8 @@ class ModelRunner:
                 topp[s] = sp.top_p if sp.top_p is not None else 1.0
                 minp[s] = sp.min_p or 0.0
                 seed[s] = sp.seed if sp.seed is not None else (hash(req.request_id) ^ self.seed) & 0x7FFFFFFFFFFF
-                offs[s] = len(req.output_token_ids)
+                offs[s] = len(req.output_token_ids) + req.num_pending
+                rslot[s] = req.slot
                 s += 1
         # padding rows (graph buckets): one token each, no cache write, null block
         for i in range(B, Bp):
@@ -194,6 +214,7 @@ class ModelRunner:
             minp[s] = 0.0
             seed[s] = 0
             offs[s] = 0
+            rslot[s] = self.pad_slot
             t += 1
             s += 1
         qst[Bp] = t
@@ -225,7 +246,9 @@ class ModelRunner:
             decode=decode, num_splits=splits, num_tokens=lay.T)
         samp = dict(temperature=sec("temp", S, torch.float32), top_k=sec("topk", S),
                     top_p=sec("topp", S, torch.float32), min_p=sec("minp", S, torch.float32),
-                    seeds=sec("seed", 2 * S).view(torch.int64), offsets=sec("offs", S))
+                    seeds=sec("seed", 2 * S).view(torch.int64), offsets=sec("offs", S),
+                    row_slots=sec("rslot", S))
+        fb.last_tok = self.last_tok
         return fb, samp
 
     def _forward_and_sample(self, fb: ForwardBatch, samp: dict, S: int, tok_out: torch.Tensor,
@@ -233,7 +256,8 @@ class ModelRunner:
         logits = self.model.forward(fb)
         ops.sample(logits, samp["temperature"], samp["top_k"], samp["top_p"], samp["seeds"],
                    samp["offsets"], min_p=samp["min_p"], out=tok_out[:S],
-                   out_logprob=lp_out[:S] if lp_out is not None else None)
+                   out_logprob=lp_out[:S] if lp_out is not None else None,
+                   row_slots=samp["row_slots"], last_tok=self.last_tok)
 
     # ------------------------------------------------------------------ graphs
     def capture_graphs(self):
@@ -258,6 +282,7 @@ class ModelRunner:
             h[o["lidx"][0]:o["lidx"][0] + b] = torch.arange(b, dtype=torch.int32)
             h[o["work"][0]:o["work"][0] + 2 * b] = torch.from_numpy(w.work.reshape(-1))
             h[o["topp"][0]:o["topp"][0] + b] = torch.tensor([1.0] * b).view(torch.int32)
+            h[o["rslot"][0]:o["rslot"][0] + b] = self.pad_slot
             buf.copy_(h)
             fb, samp = self._views(buf, lay, b, b, b, True, w.num_splits)
             tok = torch.zeros(b, dtype=torch.int32, device=self.device)
@@ -280,14 +305,18 @@ class ModelRunner:
         self.graphs.clear()
 
     # ------------------------------------------------------------------ execute
-    def execute(self, out: SchedulerOutput, want_logprobs: bool = False) -> tuple[np.ndarray, np.ndarray | None]:
-        """Run one step; returns sampled tokens (and logprobs) of the sampling rows in order."""
+    def launch(self, out: SchedulerOutput, want_logprobs: bool = False) -> "StepHandle":
+        """Enqueue one step (inputs H2D, forward, sampling, tokens D2H) without waiting."""
         B = len(out.scheduled)
         if B == 0:
-            return np.zeros(0, dtype=np.int32), None
+            return StepHandle(None, None, None, 0)
         if out.num_tokens > self.max_tokens:
             raise ValueError(f"batch of {out.num_tokens} tokens exceeds max_num_batched_tokens")
         S = sum(1 for s in out.scheduled if s.samples)
+        self._buf_idx ^= 1
+        self.host_buf = self.host_bufs[self._buf_idx]
+        self.host_np = self.host_buf.numpy()
+        tok_host, lp_host = self.tok_hosts[self._buf_idx], self.lp_hosts[self._buf_idx]
         bucket = None
         if self.use_graphs and out.is_pure_decode and self.graphs:
             for bb in sorted(self.graphs):
@@ -321,19 +350,41 @@ class ModelRunner:
             self.num_eager_steps += 1
             tok_src, lp_src = self.tok_dev, self.lp_dev
         if S == 0:
-            return np.zeros(0, dtype=np.int32), None
-        self.tok_host[:S].copy_(tok_src[:S], non_blocking=self.is_cuda)
+            return StepHandle(None, None, None, 0)
+        tok_host[:S].copy_(tok_src[:S], non_blocking=self.is_cuda)
         self.d2h_bytes += S * 4
+        lps = None
         if want_logprobs:
-            self.lp_host[:S].copy_(lp_src[:S], non_blocking=self.is_cuda)
+            lp_host[:S].copy_(lp_src[:S], non_blocking=self.is_cuda)
             self.d2h_bytes += S * 4
+            lps = lp_host
+        ev = None
         if self.is_cuda:
-            torch.cuda.current_stream(self.device).synchronize()
-        toks = self.tok_host[:S].numpy().copy()
-        lps = self.lp_host[:S].numpy().copy() if want_logprobs else None
-        return toks, lps
+            ev = torch.cuda.Event()
+            ev.record()
+        return StepHandle(ev, tok_host, lps, S)
+
+    def execute(self, out: SchedulerOutput, want_logprobs: bool = False) -> tuple[np.ndarray, np.ndarray | None]:
+        """Run one step synchronously; returns sampled tokens (and logprobs) in row order."""
+        return self.launch(out, want_logprobs).result()
 
     def _max_work_for(self, out: SchedulerOutput) -> int:
         m = self.model
         G = max(1, m.Hq // m.Hkv)
         return sum(math.ceil(s.num_tokens * G / ops.attention.PREFILL_ROWS) for s in out.scheduled) + 1
+
+
+class StepHandle:
+    """Result of a launched step; ``result()`` waits for its device->host copy."""
+
+    def __init__(self, event, tok_host, lp_host, n: int):
+        self.event, self.tok_host, self.lp_host, self.n = event, tok_host, lp_host, n
+
+    def result(self) -> tuple[np.ndarray, np.ndarray | None]:
+        if self.n == 0:
+            return np.zeros(0, dtype=np.int32), None
+        if self.event is not None:
+            self.event.synchronize()
+        toks = self.tok_host[:self.n].numpy().copy()
+        lps = self.lp_host[:self.n].numpy().copy() if self.lp_host is not None else None
+        return toks, lps
