@@ -244,6 +244,8 @@ def main():
             "p50_tpot_ms": round(float(np.median(tpot)) * 1e3, 3) if tpot else None,
             "clocks": clk, "e2e": e2e, "gpu_launches": int(gpu_launches),
             "graph_replays": r0.num_graph_replays, "eager_steps": r0.num_eager_steps,
+            "device_status": int(ext().read_status()),
+            "fused_tp_comm": eng.model.tp_fused is not None,
         }
         print(json.dumps(line), flush=True)
     llm.shutdown()

@@ -90,6 +90,10 @@ class LLMEngine:
             self.model.init_random(seed=args.seed)
         else:
             load_checkpoint_into(self.model, self.model_path)
+        if tp.world > 1 and self.device.type == "cuda" and self.b200_config.fused_comm:
+            from ..parallel import state as ps
+
+            self.model.enable_fused_comm(ps.get_parallel_state().cpu)
         self.runner = ModelRunner(self.model, max_num_seqs=args.max_num_seqs,
                                   max_num_batched_tokens=max_tok, max_model_len=self.max_model_len,
                                   block_size=args.block_size,

@@ -114,6 +114,7 @@ class LlamaForCausalLM(torch.nn.Module):
                                          cfg.rope_scaling, device=self.device)
         self.kv_caches: list[tuple[torch.Tensor, torch.Tensor]] = []
         self._alloc_workspace(max_tokens, max_decode_tokens, max_seqs)
+        self.tp_fused = None  # TPFusedComm: fused reduce-scatter / all-gather decode path
 
     # ---------------------------------------------------------------- init / weights
     def _alloc_workspace(self, max_tokens, max_dec, max_seqs):
@@ -152,6 +153,13 @@ class LlamaForCausalLM(torch.nn.Module):
             else:
                 prm.normal_(0.0, std, generator=g)
 
+    def enable_fused_comm(self, cpu_group=None):
+        """Use the fused GEMM + reduce-scatter / norm + all-gather kernels for TP decode."""
+        if self.tp.world > 1 and self.device.type == "cuda":
+            from ..parallel.fused import TPFusedComm
+
+            self.tp_fused = TPFusedComm(self.tp, self.H, self.max_decode_tokens, self.device, cpu_group)
+
     def bind_kv_cache(self, kv_caches: list[tuple[torch.Tensor, torch.Tensor]]):
         assert len(kv_caches) == self.cfg.num_layers
         self.kv_caches = kv_caches
@@ -168,9 +176,10 @@ class LlamaForCausalLM(torch.nn.Module):
         """Returns logits ``[len(logits_indices), V]`` (bf16, full vocab on every rank)."""
         T = b.num_tokens
         small = T <= self.max_decode_tokens
+        fused = small and self.tp_fused is not None
         tp = self.tp
         res = self.ws_residual[:T]
-        x = self.ws_x[:T]
+        x = self.tp_fused.x[:T] if fused else self.ws_x[:T]
         ops.embedding(b.input_ids, self.embed, self.vocab_start, self.vocab_start + self.V_local, out=res,
                       last_tok=b.last_tok)
         tp.all_reduce_(res)
@@ -198,7 +207,9 @@ class LlamaForCausalLM(torch.nn.Module):
             attn = self.ws_attn[:T]
             self._attention(q, attn, k_cache, v_cache, b)
             nxt_norm = ly.post_norm
-            if small:
+            if fused:
+                x = self.tp_fused.rs_norm(attn, ly.o, res, nxt_norm, self.eps)
+            elif small:
                 acc = self.acc_h[:T]
                 L.gemm_accumulate(attn, ly.o, acc)
                 tp.all_reduce_(acc)
@@ -213,10 +224,13 @@ class LlamaForCausalLM(torch.nn.Module):
                 acc = self.acc_gu[:T]
                 L.gemm_accumulate(x, ly.gate_up, acc)
                 act = ops.silu_mul(acc, out=self.ws_act[:T], blk=self.silu_blk, clear_input=True)
-                acc = self.acc_h[:T]
-                L.gemm_accumulate(act, ly.down, acc)
-                tp.all_reduce_(acc)
-                ops.add_rmsnorm(acc, res, nxt_norm, self.eps, out=x, clear_x=True)
+                if fused:
+                    x = self.tp_fused.rs_norm(act, ly.down, res, nxt_norm, self.eps)
+                else:
+                    acc = self.acc_h[:T]
+                    L.gemm_accumulate(act, ly.down, acc)
+                    tp.all_reduce_(acc)
+                    ops.add_rmsnorm(acc, res, nxt_norm, self.eps, out=x, clear_x=True)
             else:
                 if self.silu_blk:
                     act = L.gemm_silu(x, ly.gate_up, out=self.ws_act[:T])
