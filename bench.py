@@ -102,9 +102,14 @@ def reference_arm(args):
     else:
         sys.path.insert(0, ref_dir)
         try:
+            import importlib.util
+
             import vllm_neuron  # noqa: F401
-            why = ("vllm-neuron needs AWS Neuron devices and its libtorch_neuronx_lite/nkilib "
-                   "runtime (not in this image); it cannot execute on B200")
+            missing = [m for m in ("libtorch_neuronx_lite", "nkilib", "neuronxcc")
+                       if importlib.util.find_spec(m) is None]
+            why = ("vllm-neuron is installed (baseline/_ref) but executes only on AWS Neuron "
+                   "devices through libtorch_neuronx_lite/nkilib/neuronx-cc; missing here: "
+                   + (", ".join(missing) if missing else "a Neuron device"))
         except Exception as e:
             why = f"vllm-neuron import failed: {type(e).__name__}: {str(e)[:160]}"
     rank = int(os.environ.get("RANK", "0"))

@@ -412,11 +412,8 @@ static void launch_attn(const PagedAttnParams& p, int num_work, cudaStream_t str
   static_assert(!DECODE || (2 * 4 * 16 + 4 * 16 * D) * 4 <= 4 * kKvTile * D * 2,
                 "decode merge scratch must fit in the K/V tiles");
   auto kern = paged_attention_kernel<D, DECODE>;
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    configured = true;
-  }
+  static std::atomic<uint64_t> configured{0};
+  set_max_dynamic_smem_once(kern, smem, configured);
   dim3 grid(num_work, p.Hkv, p.num_splits);
   launch_pdl(kern, grid, dim3(128), smem, stream, p);
 }

@@ -12,6 +12,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <utility>
 
 #ifndef B200_WAIT_TIMEOUT_NS
@@ -344,6 +345,20 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// Raises a kernel's dynamic shared memory limit once per device.  Function attributes
+// belong to the device's context, so a process that drives several GPUs must set them on
+// each; `done` is a per-instantiation bitmask of the devices already configured.
+template <typename... KArgs>
+inline void set_max_dynamic_smem_once(void (*kernel)(KArgs...), int smem,
+                                      std::atomic<uint64_t>& done) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+  const uint64_t bit = 1ull << dev;
+  if (done.load(std::memory_order_acquire) & bit) return;
+  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  done.fetch_or(bit, std::memory_order_acq_rel);
 }
 #endif
 

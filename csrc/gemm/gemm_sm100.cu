@@ -473,11 +473,8 @@ static void launch_impl(const CUtensorMap& ta, const CUtensorMap& tb, const Gemm
                         int grid, cudaStream_t stream) {
   constexpr int smem = STAGES * (kATileBytes + BN * kBK * 2) + 1024 + 256;
   auto kern = gemm_bf16_kernel<BN, STAGES, EPI>;
-  static bool configured = false;  // one attribute call per instantiation
-  if (!configured) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    configured = true;
-  }
+  static std::atomic<uint64_t> configured{0};  // per instantiation, per device
+  set_max_dynamic_smem_once(kern, smem, configured);
   launch_pdl(kern, dim3(grid), dim3(192), smem, stream, ta, tb, p);
 }
 
