@@ -3,6 +3,10 @@ overhead: a decode step of B sequences at context L replayed from its CUDA graph
 eager prefill chunk of T tokens.  Also reports the host time of batch preparation.
 
     python benchmarks/bench_step.py [--batch 64] [--ctx 1152] [--chunk 8192] [--layers 32]
+    torchrun --nproc-per-node N --master-addr 127.0.0.1 benchmarks/bench_step.py ...   (TP=N)
+    python benchmarks/bench_step.py --emulate-tp N     (one GPU runs rank 0's share of TP=N)
+
+With TP, times are the maximum over ranks.
 """
 from __future__ import annotations
 
@@ -32,17 +36,35 @@ def main():
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--json", type=str, default=None)
+    ap.add_argument("--no-fused", action="store_true", help="TP: NCCL all-reduce instead of the fused kernel")
+    ap.add_argument("--emulate-tp", type=int, default=1,
+                    help="one GPU runs rank 0's share of TP=N with local no-op collectives (profiling only)")
     ap.add_argument("--profile-once", action="store_true",
                     help="run one decode replay and one prefill chunk inside NVTX ranges "
                          "'decode_step' / 'prefill_chunk' (for an ncu launch list)")
     a = ap.parse_args()
+    from vllm_neuron_b200.parallel import state as ps
+
+    rank, world = ps.init_distributed(timeout_s=300)
+    if world > 1:
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
     cfg = dict(LLAMA3_8B, num_hidden_layers=a.layers)
     B, L = a.batch, a.ctx
     max_len = max(L + 64, 2048)
     blocks = B * (max_len // 16 + 1) + 64
-    llm = LLM(cfg, max_num_seqs=B, max_model_len=max_len, max_num_batched_tokens=a.chunk,
-              load_format="dummy", num_gpu_blocks=blocks, skip_tokenizer_init=True)
-    eng = llm.engine
+    if a.emulate_tp > 1:
+        from vllm_neuron_b200.engine.llm_engine import EngineArgs, LLMEngine
+        from vllm_neuron_b200.parallel.comm import EmulatedRankComm
+
+        eng = LLMEngine(EngineArgs(model=cfg, max_num_seqs=B, max_model_len=max_len,
+                                   max_num_batched_tokens=a.chunk, load_format="dummy",
+                                   num_gpu_blocks=blocks), tp=EmulatedRankComm(a.emulate_tp))
+    else:
+        llm = LLM(cfg, tensor_parallel_size=world,
+                  additional_config={"b200_config": {"fused_comm": not a.no_fused}},
+                  max_num_seqs=B, max_model_len=max_len, max_num_batched_tokens=a.chunk,
+                  load_format="dummy", num_gpu_blocks=blocks, skip_tokenizer_init=True)
+        eng = llm.engine
     runner = eng.runner
     sp = SamplingParams(temperature=0.0, max_tokens=1 << 20, ignore_eos=True)
     # Fake B running requests at context L with contiguous block ids.
@@ -127,11 +149,25 @@ def main():
     res["prefill_tokens"] = per * n_seq
     flops = 2 * 7.5e9 * per * n_seq * a.layers / 32
     res["prefill_tflops_dense_only"] = flops / (res["prefill_chunk_ms"] * 1e9)
-    res.update(batch=B, ctx=L, layers=a.layers)
-    print(json.dumps(res), flush=True)
-    if a.json:
+    res.update(batch=B, ctx=L, layers=a.layers, tp=world, emulated_tp=a.emulate_tp)
+    if world > 1:
+        import torch.distributed as dist
+
+        keys = [k for k, v in res.items() if k.endswith("_ms")]
+        t = torch.tensor([res[k] for k in keys], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        for k, v in zip(keys, t.tolist()):
+            res[k] = v
+        res["prefill_tflops_dense_only"] = flops / (res["prefill_chunk_ms"] * 1e9)
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    if a.json and rank == 0:
         with open(a.json, "w") as f:
             json.dump(res, f)
+    sys.stdout.flush()
+    # Skip interpreter teardown (IPC mappings and NCCL communicators are released by the
+    # process exit); every rank has finished its collectives above.
+    os._exit(0)
 
 
 if __name__ == "__main__":

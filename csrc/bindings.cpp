@@ -291,66 +291,41 @@ static void fill_ptrs(const std::vector<int64_t>& v, void** dst, const char* wha
   for (size_t i = 0; i < v.size(); ++i) dst[i] = (void*)v[i];
 }
 
-// acc[T, N] += x @ w^T locally (split-K), then the completing split of every 128-column tile
-// pushes the tile's token rows to their owner ranks' receive slots.
-void gemm_tp_rs(const at::Tensor& w, const at::Tensor& x, at::Tensor& acc, int64_t splits,
-                const std::vector<int64_t>& slot_ptrs, const std::vector<int64_t>& arrive_ptrs,
-                at::Tensor& tile_count, int64_t rank, int64_t rows_per_rank) {
-  CHECK_BF16(w);
-  CHECK_BF16(x);
+// residual += all_reduce(acc) over the TP group (one-shot push through symmetric peer
+// memory), out = rmsnorm(residual) * w; acc is cleared.
+void tp_allreduce_norm(at::Tensor& acc, const std::vector<int64_t>& recv_ptrs,
+                       const std::vector<int64_t>& flag_ptrs, at::Tensor& state,
+                       at::Tensor& residual, const at::Tensor& w, at::Tensor& out, double eps,
+                       int64_t rank, int64_t max_rows) {
+  CHECK_CUDA(acc);
   TORCH_CHECK(acc.scalar_type() == at::kFloat, "acc must be fp32");
-  const c10::cuda::CUDAGuard guard(x.device());
-  b200::TPRsParams tp{};
-  fill_ptrs(slot_ptrs, (void**)tp.slots, "slots");
-  fill_ptrs(arrive_ptrs, (void**)tp.arrive, "arrive");
-  tp.tile_count = tile_count.data_ptr<int>();
-  tp.rank = (int)rank;
-  tp.world = (int)slot_ptrs.size();
-  tp.rows_per_rank = (int)rows_per_rank;
-  tp.H = (int)w.size(0);
-  b200::GemmArgs g{};
-  g.A = w.data_ptr();
-  g.B = x.data_ptr();
-  g.out = acc.data_ptr();
-  g.lda = w.stride(0);
-  g.ldb = x.stride(0);
-  g.ldo = acc.stride(0);
-  g.M = (int)w.size(0);
-  g.N = (int)x.size(0);
-  g.K = (int)w.size(1);
-  g.bn = x.size(0) <= 16 ? 16 : x.size(0) <= 32 ? 32 : x.size(0) <= 64 ? 64 : 128;
-  TORCH_CHECK(x.size(0) <= 128, "gemm_tp_rs: at most 128 tokens");
-  g.epi = b200::EPI_TP_RS;
-  g.splits = (int)splits;
-  g.status = status_word();
-  g.tp = &tp;
-  b200::gemm_bf16_launch(g, cur_stream());
-  check_launch("gemm_tp_rs");
-}
-
-void tp_norm_allgather(int64_t slots_ptr, int64_t slot_arrive_ptr,
-                       const std::vector<int64_t>& x_ptrs, const std::vector<int64_t>& x_arrive_ptrs,
-                       at::Tensor& state, at::Tensor& residual, const at::Tensor& w, double eps,
-                       int64_t rank, int64_t rows_per_rank, int64_t T, int64_t tiles_per_call) {
-  const c10::cuda::CUDAGuard guard(residual.device());
-  b200::TPNormAGParams p{};
-  p.slots = (const __nv_bfloat16*)slots_ptr;
-  p.slot_arrive = (unsigned long long*)slot_arrive_ptr;
-  fill_ptrs(x_ptrs, (void**)p.x_peers, "x");
-  fill_ptrs(x_arrive_ptrs, (void**)p.x_arrive, "x_arrive");
+  CHECK_BF16(residual);
+  CHECK_BF16(out);
+  TORCH_CHECK(recv_ptrs.size() == flag_ptrs.size(), "recv/flag pointer lists differ");
+  TORCH_CHECK(acc.stride(1) == 1 && residual.stride(1) == 1 && out.stride(1) == 1,
+              "rows must be contiguous");
+  TORCH_CHECK(acc.stride(0) % 4 == 0, "acc row stride must be a multiple of 4");
+  const c10::cuda::CUDAGuard guard(acc.device());
+  b200::TPArNormParams p{};
+  p.acc = acc.data_ptr<float>();
+  p.acc_stride = acc.stride(0);
+  fill_ptrs(recv_ptrs, (void**)p.recv_peers, "recv");
+  fill_ptrs(flag_ptrs, (void**)p.flag_peers, "flags");
   p.state = (unsigned long long*)state.data_ptr<int64_t>();
   p.residual = reinterpret_cast<__nv_bfloat16*>(residual.data_ptr());
+  p.res_stride = residual.stride(0);
   p.w = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
+  p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  p.out_stride = out.stride(0);
   p.status = status_word();
   p.eps = (float)eps;
   p.rank = (int)rank;
-  p.world = (int)x_ptrs.size();
-  p.rows_per_rank = (int)rows_per_rank;
-  p.H = (int)w.size(0);
-  p.T = (int)T;
-  p.tiles_per_call = (int)tiles_per_call;
-  b200::tp_norm_allgather_launch(p, cur_stream());
-  check_launch("tp_norm_allgather");
+  p.world = (int)recv_ptrs.size();
+  p.max_rows = (int)max_rows;
+  p.H = (int)acc.size(1);
+  p.T = (int)acc.size(0);
+  b200::tp_allreduce_norm_launch(p, cur_stream());
+  check_launch("tp_allreduce_norm", p.T > 0 ? 1 : 0);
 }
 
 int64_t num_sms() { return b200::num_sms_cached(); }
@@ -377,6 +352,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_close", &symm_close);
   m.def("symm_free", &symm_free);
   m.def("tensor_from_ptr", &tensor_from_ptr);
-  m.def("gemm_tp_rs", &gemm_tp_rs);
-  m.def("tp_norm_allgather", &tp_norm_allgather);
+  m.def("tp_allreduce_norm", &tp_allreduce_norm);
 }

@@ -15,30 +15,26 @@ void symm_free(void* p);
 
 constexpr int kMaxTP = 8;
 
-// Reduce-scatter target of the fused row-parallel GEMM (EPI_TP_RS) and input of
-// tp_norm_allgather: rank r owns token rows [r * rpr, (r + 1) * rpr).
-struct TPRsParams {
-  __nv_bfloat16* slots[kMaxTP];        // per rank: [world][rpr][H] bf16 receive slots
-  unsigned long long* arrive[kMaxTP];  // per rank: slot-arrival counter (64-bit, cumulative)
-  int* tile_count;                     // local: contributions received per output tile
-  int rank, world, rows_per_rank, H;
-  int splits;                          // contributions per tile (split-K factor)
-};
-
-struct TPNormAGParams {
-  const __nv_bfloat16* slots;          // local receive slots [world][rpr][H]
-  unsigned long long* slot_arrive;     // local slot-arrival counter
-  __nv_bfloat16* x_peers[kMaxTP];      // per rank: all-gathered normalized rows [T][H]
-  unsigned long long* x_arrive[kMaxTP];  // per rank: row-arrival counter
-  unsigned long long* state;           // local: [0] calls completed, [1] CTAs done this call
-  __nv_bfloat16* residual;             // local [T][H] (owned rows are updated)
-  const __nv_bfloat16* w;              // RMSNorm weight [H]
+// One-shot all-reduce of a row-parallel projection's fp32 partial sums, fused with the
+// residual add and the next RMSNorm (tp_fused.cu).  Every rank pushes its bf16 partial rows
+// into every peer's receive slots over NVLink, publishes one flag per (row, source) and
+// sums the world's partials in rank order, so all ranks hold bitwise-identical results.
+struct TPArNormParams {
+  float* acc;                           // local [T][H] fp32 partials (cleared by the kernel)
+  long long acc_stride;
+  __nv_bfloat16* recv_peers[kMaxTP];    // per rank: receive slots [2][world][max_rows][H]
+  unsigned int* flag_peers[kMaxTP];     // per rank: flags [2][max_rows][world] (epoch numbers)
+  unsigned long long* state;            // local: [0] calls completed, [1] CTAs done this call
+  __nv_bfloat16* residual;              // local [T][H], updated in place (all rows)
+  long long res_stride;
+  const __nv_bfloat16* w;               // RMSNorm weight [H]
+  __nv_bfloat16* out;                   // local [T][H] normalized activations
+  long long out_stride;
   uint32_t* status;
   float eps;
-  int rank, world, rows_per_rank, H, T;
-  int tiles_per_call;                  // output tiles per rank per GEMM (N / 128)
+  int rank, world, max_rows, H, T;
 };
 
-void tp_norm_allgather_launch(const TPNormAGParams& p, cudaStream_t stream);
+void tp_allreduce_norm_launch(const TPArNormParams& p, cudaStream_t stream);
 
 }  // namespace b200

@@ -1,19 +1,26 @@
-// Second half of the fused row-parallel projection for tensor-parallel decode:
+// Fused tensor-parallel all-reduce + residual add + RMSNorm for decode-sized batches.
 //
-//   GEMM (EPI_TP_RS)      each rank pushes its partial rows to the rows' owners (NVLink)
-//   tp_norm_allgather     owner: sum the world partials + residual, RMSNorm, and store the
-//                         normalized row into every rank's activation buffer (NVLink), then
-//                         wait until all rows of this call have arrived from every owner.
-//
-// This replaces "GEMM -> all-reduce -> residual add -> RMSNorm" (reference:
+// Replaces "row-parallel GEMM -> all-reduce -> residual add -> RMSNorm" (reference:
 // RowParallelLinear + all-reduce, vllm_neuron/nn/rpl.py:23-154, and the decode all-reduce
-// sites in vllm_neuron/model/llama3/model.py:989,1113) with one reduce-scatter fused into the
-// GEMM epilogue and one all-gather fused into the norm.  The residual stream of a rank is
-// only kept for the rows it owns (sequence-parallel residual).
+// sites of vllm_neuron/model/llama3/model.py:989,1113) after the local split-K GEMM has
+// accumulated this rank's fp32 partial sums.  One CTA per token row:
 //
-// Synchronization: cumulative 64-bit arrival counters in symmetric memory, release/acquire
-// at system scope, and a per-rank call counter kept on the device (CUDA-graph safe).  Every
-// wait is bounded by %globaltimer; on expiry the kernel records a status code and returns.
+//   1. read the fp32 partial row, clear it, round it to bf16 and store it into the receive
+//      slot [parity][this rank][row] of every other rank (NVLink stores through CUDA-IPC
+//      mapped symmetric memory);
+//   2. fence at system scope, then release-store flag [parity][row][this rank] = epoch + 1 on
+//      every rank;
+//   3. wait (bounded) until every peer's flag for this row has reached epoch + 1;
+//   4. residual += sum of the world's bf16 partials in rank order 0..world-1 (identical on
+//      every rank), RMSNorm, and store the normalized row locally.
+//
+// Slots and flags alternate between two parities by call number: a rank can only be one call
+// ahead of a peer (it needs that peer's flags to finish a call), so the parity it writes is
+// never one the peer is still reading.  The call counter lives on the device (state[0]) so
+// captured CUDA graphs replay correctly; the grid's last CTA advances it.  The signal count
+// per call does not depend on the batch size, so consecutive calls may differ in T.  Every
+// wait is bounded by %globaltimer; on expiry the kernel records a status code and carries on,
+// and once the status is set later waits return at once (the host checks the status).
 #include <cuda_bf16.h>
 
 #include <stdexcept>
@@ -23,138 +30,170 @@
 
 namespace b200 {
 
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+__device__ __forceinline__ unsigned int ld_acquire_sys_u32(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ void st_release_sys_u32(unsigned int* p, unsigned int v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 
-// Returns false (and records `code`) if the counter did not reach `target` in time.
-__device__ __forceinline__ bool wait_counter(const unsigned long long* c, unsigned long long target,
-                                             uint32_t* status, uint32_t code) {
-  if (ld_acquire_sys(c) >= target) return true;
+// Returns false (and records `code`) if *f did not reach `target` in time.
+__device__ __forceinline__ bool wait_flag(const unsigned int* f, unsigned int target,
+                                          uint32_t* status, uint32_t code) {
+  if ((int)(ld_acquire_sys_u32(f) - target) >= 0) return true;
+  if (status != nullptr && *reinterpret_cast<volatile uint32_t*>(status) != 0u) return false;
   const uint64_t t0 = globaltimer_ns();
-  while (ld_acquire_sys(c) < target) {
+  while ((int)(ld_acquire_sys_u32(f) - target) < 0) {
     if (globaltimer_ns() - t0 > B200_WAIT_TIMEOUT_NS) {
       set_status(status, code);
       return false;
     }
-    __nanosleep(64);
+    __nanosleep(32);
   }
   return true;
 }
 
 template <int NV>
-__global__ void __launch_bounds__(256) tp_norm_allgather_kernel(const TPNormAGParams p) {
+__global__ void __launch_bounds__(256) tp_allreduce_norm_kernel(const TPArNormParams p) {
   pdl_trigger();
   pdl_wait();
-  __shared__ float red[32];
-  __shared__ unsigned long long epoch_s;
+  __shared__ float red[8];
+  __shared__ unsigned int epoch_s;
   const int tid = threadIdx.x;
-  if (tid == 0) {
-    const unsigned long long e = *reinterpret_cast<volatile unsigned long long*>(&p.state[0]);
-    epoch_s = e;
-    wait_counter(p.slot_arrive, (e + 1) * (unsigned long long)(p.tiles_per_call * p.world),
-                 p.status, kTimeoutPeerFlag);
-  }
+  const int row = blockIdx.x;
+  if (tid == 0) epoch_s = (unsigned int)*reinterpret_cast<volatile unsigned long long*>(&p.state[0]);
   __syncthreads();
-  const unsigned long long e = epoch_s;
-  const int lrow = blockIdx.x;
-  const int gm = p.rank * p.rows_per_rank + lrow;
-  if (lrow < p.rows_per_rank && gm < p.T) {
-    float v[NV][8];
-    float ss = 0.f;
+  const unsigned int e = epoch_s;
+  const int par = (int)(e & 1u);
+  const long long slot_rows = (long long)p.world * p.max_rows;
+  const long long row_off = ((long long)par * slot_rows + (long long)p.rank * p.max_rows + row) * p.H;
+
+  // 1. partial row: fp32 -> bf16, cleared, pushed to every other rank's slot
+  uint4 mine[NV];
 #pragma unroll
-    for (int j = 0; j < NV; ++j) {
-      const int idx = (j * blockDim.x + tid) * 8;
-      if (idx < p.H) {
-        float acc[8];
-        const uint4 r = *reinterpret_cast<const uint4*>(p.residual + (long long)gm * p.H + idx);
-        const uint32_t rw[4] = {r.x, r.y, r.z, r.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 f = unpack_bf16x2(rw[i]);
-          acc[2 * i] = f.x;
-          acc[2 * i + 1] = f.y;
-        }
-        for (int w = 0; w < p.world; ++w) {
-          const uint4 s = __ldcg(reinterpret_cast<const uint4*>(
-              p.slots + ((long long)(w * p.rows_per_rank + lrow)) * p.H + idx));
-          const uint32_t sw[4] = {s.x, s.y, s.z, s.w};
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float2 f = unpack_bf16x2(sw[i]);
-            acc[2 * i] += f.x;
-            acc[2 * i + 1] += f.y;
-          }
-        }
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          v[j][k] = __bfloat162float(__float2bfloat16(acc[k]));
-          ss += v[j][k] * v[j][k];
-        }
-        *reinterpret_cast<uint4*>(p.residual + (long long)gm * p.H + idx) =
-            make_uint4(pack_bf16x2(v[j][0], v[j][1]), pack_bf16x2(v[j][2], v[j][3]),
-                       pack_bf16x2(v[j][4], v[j][5]), pack_bf16x2(v[j][6], v[j][7]));
-      }
-    }
-    ss = warp_sum(ss);
-    if ((tid & 31) == 0) red[tid >> 5] = ss;
-    __syncthreads();
-    float t = (tid < (int)(blockDim.x >> 5)) ? red[tid] : 0.f;
-    if (tid < 32) {
-      t = warp_sum(t);
-      if (tid == 0) red[0] = t;
-    }
-    __syncthreads();
-    const float inv = rsqrtf(red[0] / (float)p.H + p.eps);
-#pragma unroll
-    for (int j = 0; j < NV; ++j) {
-      const int idx = (j * blockDim.x + tid) * 8;
-      if (idx < p.H) {
-        const uint4 g = *reinterpret_cast<const uint4*>(p.w + idx);
-        const uint32_t gw[4] = {g.x, g.y, g.z, g.w};
-        uint32_t o[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 f = unpack_bf16x2(gw[i]);
-          o[i] = pack_bf16x2(v[j][2 * i] * inv * f.x, v[j][2 * i + 1] * inv * f.y);
-        }
-        const uint4 ov = make_uint4(o[0], o[1], o[2], o[3]);
-        for (int r = 0; r < p.world; ++r)
-          *reinterpret_cast<uint4*>(p.x_peers[r] + (long long)gm * p.H + idx) = ov;
-      }
+  for (int j = 0; j < NV; ++j) {
+    const int idx = (j * 256 + tid) * 8;
+    if (idx < p.H) {
+      float4* src = reinterpret_cast<float4*>(p.acc + (long long)row * p.acc_stride + idx);
+      const float4 a = src[0], b = src[1];
+      src[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+      src[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+      mine[j] = make_uint4(pack_bf16x2(a.x, a.y), pack_bf16x2(a.z, a.w), pack_bf16x2(b.x, b.y),
+                           pack_bf16x2(b.z, b.w));
+      for (int r = 0; r < p.world; ++r)
+        if (r != p.rank) *reinterpret_cast<uint4*>(p.recv_peers[r] + row_off + idx) = mine[j];
     }
   }
   __threadfence_system();
   __syncthreads();
+  // 2. publish, 3. wait for every peer's row
+  if (tid < p.world) {
+    st_release_sys_u32(p.flag_peers[tid] + ((long long)par * p.max_rows + row) * p.world + p.rank,
+                       e + 1u);
+  }
+  if (tid < p.world && tid != p.rank) {
+    const unsigned int* f = p.flag_peers[p.rank] + ((long long)par * p.max_rows + row) * p.world + tid;
+    wait_flag(f, e + 1u, p.status, kTimeoutPeerFlag);
+  }
+  __syncthreads();
+  // 4. residual += sum of partials (rank order), RMSNorm
+  const __nv_bfloat16* recv = p.recv_peers[p.rank];
+  float v[NV][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int idx = (j * 256 + tid) * 8;
+    if (idx < p.H) {
+      float acc[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+      for (int r = 0; r < p.world; ++r) {
+        uint4 s;
+        if (r == p.rank) {
+          s = mine[j];
+        } else {
+          s = __ldcv(reinterpret_cast<const uint4*>(
+              recv + ((long long)par * slot_rows + (long long)r * p.max_rows + row) * p.H + idx));
+        }
+        const uint32_t sw[4] = {s.x, s.y, s.z, s.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = unpack_bf16x2(sw[i]);
+          acc[2 * i] += f.x;
+          acc[2 * i + 1] += f.y;
+        }
+      }
+      __nv_bfloat16* res = p.residual + (long long)row * p.res_stride + idx;
+      const uint4 rv = *reinterpret_cast<const uint4*>(res);
+      const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = unpack_bf16x2(rw[i]);
+        // the all-reduced projection is rounded to bf16 before the residual add
+        v[j][2 * i] = __bfloat162float(__float2bfloat16(acc[2 * i])) + f.x;
+        v[j][2 * i + 1] = __bfloat162float(__float2bfloat16(acc[2 * i + 1])) + f.y;
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        v[j][k] = __bfloat162float(__float2bfloat16(v[j][k]));
+        ss += v[j][k] * v[j][k];
+      }
+      *reinterpret_cast<uint4*>(res) =
+          make_uint4(pack_bf16x2(v[j][0], v[j][1]), pack_bf16x2(v[j][2], v[j][3]),
+                     pack_bf16x2(v[j][4], v[j][5]), pack_bf16x2(v[j][6], v[j][7]));
+    }
+  }
+  ss = warp_sum(ss);
+  if ((tid & 31) == 0) red[tid >> 5] = ss;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) t += red[w];
+  const float inv = rsqrtf(t / (float)p.H + p.eps);
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int idx = (j * 256 + tid) * 8;
+    if (idx < p.H) {
+      const uint4 g = *reinterpret_cast<const uint4*>(p.w + idx);
+      const uint32_t gw[4] = {g.x, g.y, g.z, g.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = unpack_bf16x2(gw[i]);
+        o[i] = pack_bf16x2(v[j][2 * i] * inv * f.x, v[j][2 * i + 1] * inv * f.y);
+      }
+      *reinterpret_cast<uint4*>(p.out + (long long)row * p.out_stride + idx) =
+          make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+  // the grid's last CTA advances the call counter
   if (tid == 0) {
-    for (int r = 0; r < p.world; ++r) atomicAdd_system(p.x_arrive[r], 1ull);
-    // all rows of this call, from every owner
-    wait_counter(p.x_arrive[p.rank], (e + 1) * (unsigned long long)(p.world * p.rows_per_rank),
-                 p.status, kTimeoutPeerFlag);
     __threadfence();
     if (atomicAdd(&p.state[1], 1ull) == (unsigned long long)(gridDim.x - 1)) {
       p.state[1] = 0;
       __threadfence();
-      p.state[0] = e + 1;
+      p.state[0] = (unsigned long long)e + 1ull;
     }
   }
 }
 
-void tp_norm_allgather_launch(const TPNormAGParams& p, cudaStream_t stream) {
-  if (p.H % 8 != 0) throw std::invalid_argument("tp_norm_allgather: H must be a multiple of 8");
-  const int vecs = p.H / 8;
-  const int nv = (vecs + 255) / 256;
-  const dim3 grid(p.rows_per_rank > 0 ? p.rows_per_rank : 1);
+void tp_allreduce_norm_launch(const TPArNormParams& p, cudaStream_t stream) {
+  if (p.H % 8 != 0) throw std::invalid_argument("tp_allreduce_norm: H must be a multiple of 8");
+  if (p.T > p.max_rows) throw std::invalid_argument("tp_allreduce_norm: too many rows");
+  if (p.world < 2 || p.world > kMaxTP) throw std::invalid_argument("tp_allreduce_norm: bad world");
+  if (p.T == 0) return;
+  const int nv = (p.H / 8 + 255) / 256;
+  const dim3 grid(p.T);
   if (nv <= 1)
-    launch_pdl(tp_norm_allgather_kernel<1>, grid, dim3(256), 0, stream, p);
+    launch_pdl(tp_allreduce_norm_kernel<1>, grid, dim3(256), 0, stream, p);
   else if (nv <= 2)
-    launch_pdl(tp_norm_allgather_kernel<2>, grid, dim3(256), 0, stream, p);
+    launch_pdl(tp_allreduce_norm_kernel<2>, grid, dim3(256), 0, stream, p);
   else if (nv <= 4)
-    launch_pdl(tp_norm_allgather_kernel<4>, grid, dim3(256), 0, stream, p);
+    launch_pdl(tp_allreduce_norm_kernel<4>, grid, dim3(256), 0, stream, p);
   else
-    throw std::invalid_argument("tp_norm_allgather: hidden size too large");
+    throw std::invalid_argument("tp_allreduce_norm: hidden size too large");
 }
 
 }  // namespace b200

@@ -139,7 +139,7 @@ __device__ __forceinline__ bool mbar_wait_abortable(uint64_t* bar, uint32_t pari
 }
 
 // ----------------------------------------------------------------------------------------
-// TMA (no multicast anywhere in this library)
+// TMA tile loads (plain, single-CTA destination)
 // ----------------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const void* desc) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(desc) : "memory");

@@ -4,8 +4,6 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#include "../comm/symm_mem.h"
-
 namespace b200 {
 
 enum GemmEpilogue : int {
@@ -14,8 +12,6 @@ enum GemmEpilogue : int {
   EPI_F32_RED = 2,    // out[m, n] += D          (fp32 reduction, split-K)
   EPI_F32_RED_T = 3,  // out[n, m] += D          (fp32 reduction, swapped operands)
   EPI_SILU_BF16 = 4,  // out[m, j] = silu(gate) * up, gate/up interleaved per BN tile
-  EPI_TP_RS = 5,      // out[n, m] += D locally, then the last split of each tile pushes the
-                      // tile's token rows (bf16) to their owner ranks (fused reduce-scatter)
 };
 
 struct GemmArgs {
@@ -30,7 +26,6 @@ struct GemmArgs {
   int group_m;    // rasterization group along M (0 = default)
   int max_ctas;   // cap on persistent CTAs (0 = number of SMs)
   uint32_t* status;  // device status word for bounded-wait failures (may be null)
-  const TPRsParams* tp;  // EPI_TP_RS only
 };
 
 void gemm_bf16_launch(const GemmArgs& args, cudaStream_t stream);

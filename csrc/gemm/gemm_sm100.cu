@@ -47,7 +47,6 @@ struct GemmParams {
   void* out;
   long long ldo;
   uint32_t* status;
-  TPRsParams tp;  // EPI_TP_RS only
 };
 
 __device__ __forceinline__ void decode_tile(const GemmParams& p, int tile, int& mb, int& nb,
@@ -99,45 +98,6 @@ struct SegCursor {
   }
 };
 
-// Fused reduce-scatter (EPI_TP_RS, swapped operands: the tile is 128 output columns of every
-// token row).  Each split has added its partial sums into the local fp32 buffer; the split
-// that completes a tile reads it back, clears it, and stores every token row's 128 columns
-// (bf16) into the receive slot of the rank that owns that row, over NVLink.  It then
-// signals every rank once (uniform counts: tiles_per_call * world arrivals per call).
-template <int BN>
-__device__ __forceinline__ void tp_rs_fixup(const GemmParams& p, int tile, int row, int* flag) {
-  const int et = threadIdx.x - 64;  // 0..127 over the four epilogue warps
-  __threadfence();
-  asm volatile("bar.sync 1, 128;" ::: "memory");
-  if (et == 0) {
-    const int old = atomicAdd(&p.tp.tile_count[tile], 1);
-    const int last = (old == p.tp.splits - 1);
-    if (last) p.tp.tile_count[tile] = 0;
-    *flag = last;
-  }
-  asm volatile("bar.sync 1, 128;" ::: "memory");
-  if (!*flag) return;
-  __threadfence();
-  const int n = tile * 128 + row;  // output column owned by this thread
-  if (n < p.M) {
-    float* col = reinterpret_cast<float*>(p.out) + n;
-    for (int m = 0; m < p.N; ++m) {
-      float* src = col + (long long)m * p.ldo;
-      const float v = __ldcg(src);
-      *src = 0.f;
-      const int owner = m / p.tp.rows_per_rank;
-      const int lrow = m - owner * p.tp.rows_per_rank;
-      __nv_bfloat16* dst = p.tp.slots[owner] +
-                           ((long long)(p.tp.rank * p.tp.rows_per_rank + lrow)) * p.tp.H + n;
-      *dst = __float2bfloat16(v);
-    }
-  }
-  __threadfence_system();
-  asm volatile("bar.sync 1, 128;" ::: "memory");
-  if (et == 0) {
-    for (int r = 0; r < p.tp.world; ++r) atomicAdd_system(p.tp.arrive[r], 1ull);
-  }
-}
 
 template <int BN>
 struct TmemCols {
@@ -168,7 +128,6 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* tempty_bar = tfull_bar + 2;
   uint32_t* tmem_base_smem = reinterpret_cast<uint32_t*>(tempty_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_smem + 1);
-  int* tile_flag = reinterpret_cast<int*>(tmem_base_smem + 2);
 
   const int warp = warp_id();
   const int lane = lane_id();
@@ -199,7 +158,7 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 0) {
     // ------------------------------ TMA producer ------------------------------
     if (elect_one()) {
-      constexpr bool kWeightIsA = (EPI == EPI_BF16_T || EPI == EPI_F32_RED_T || EPI == EPI_TP_RS);
+      constexpr bool kWeightIsA = (EPI == EPI_BF16_T || EPI == EPI_F32_RED_T);
       const uint64_t hint_a = kWeightIsA ? policy_evict_first()  // A = weights, streamed once
                                          : policy_evict_last();
       const uint64_t hint_b = kWeightIsA ? policy_evict_last()   // B = activations, reused
@@ -408,7 +367,7 @@ __global__ void __launch_bounds__(192, 1)
                   if (n0 + j < p.N) atomicAdd(o + j, __uint_as_float(r[j]));
               }
             }
-          } else {  // EPI_F32_RED_T and EPI_TP_RS: fp32 reductions into out[n, m]
+          } else {  // EPI_F32_RED_T: fp32 reductions into out[n, m]
             if (m < p.M) {
               float* o = reinterpret_cast<float*>(p.out) + m;
 #pragma unroll
@@ -421,7 +380,6 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty_bar[acc]);
-      if constexpr (EPI == EPI_TP_RS) tp_rs_fixup<BN>(p, mb, row, tile_flag);
     }
   }
 
@@ -508,19 +466,12 @@ void gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
   if (splits > p.num_k_blocks) splits = p.num_k_blocks;
   p.kb_per_split = (p.num_k_blocks + splits - 1) / splits;
   p.splits = (p.num_k_blocks + p.kb_per_split - 1) / p.kb_per_split;  // no empty split
-  if (a.epi == EPI_TP_RS && p.streamk)
-    throw std::invalid_argument("gemm: EPI_TP_RS uses fixed split-K, not stream-K");
-  if ((p.splits > 1 || p.streamk) && (a.epi != EPI_F32_RED && a.epi != EPI_F32_RED_T && a.epi != EPI_TP_RS))
+  if ((p.splits > 1 || p.streamk) && (a.epi != EPI_F32_RED && a.epi != EPI_F32_RED_T))
     throw std::invalid_argument("gemm: split-K / stream-K require an fp32 reduction epilogue");
   p.group_m = a.group_m > 0 ? a.group_m : 16;
   p.out = a.out;
   p.ldo = a.ldo;
   p.status = a.status;
-  if (a.epi == EPI_TP_RS) {
-    if (a.tp == nullptr) throw std::invalid_argument("gemm: EPI_TP_RS needs TP parameters");
-    p.tp = *a.tp;
-    p.tp.splits = p.splits;
-  }
   const long long tiles = (long long)p.num_m_blocks * p.num_n_blocks * p.splits;
   int grid = num_sms_cached();
   if (a.max_ctas > 0 && a.max_ctas < grid) grid = a.max_ctas;
@@ -549,10 +500,6 @@ void gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
   B200_GEMM_CASE(32, 8, EPI_F32_RED_T)
   B200_GEMM_CASE(64, 8, EPI_F32_RED_T)
   B200_GEMM_CASE(128, 6, EPI_F32_RED_T)
-  B200_GEMM_CASE(16, 8, EPI_TP_RS)
-  B200_GEMM_CASE(32, 8, EPI_TP_RS)
-  B200_GEMM_CASE(64, 8, EPI_TP_RS)
-  B200_GEMM_CASE(128, 6, EPI_TP_RS)
 #undef B200_GEMM_CASE
   throw std::invalid_argument("gemm: unsupported (bn, epilogue) combination: bn=" +
                               std::to_string(bn) + " epi=" + std::to_string(a.epi));

@@ -148,12 +148,23 @@ class LLMEngine:
             self._free_slots.append(req.slot)
             req.slot = -1
 
+    def _check_device_status(self):
+        """Raise if a bounded device wait (peer flag of a fused collective) has expired."""
+        from ..ops._ext import ext
+
+        code = int(ext().read_status())
+        if code != 0:
+            raise RuntimeError(f"device status {code}: a bounded wait of a fused collective expired "
+                               "(a peer rank stopped or fell out of step)")
+
     def has_unfinished_requests(self) -> bool:
         return self.scheduler.has_unfinished() or self._inflight is not None
 
     # ---------------------------------------------------------------- stepping
     def _process(self, out, handle) -> list[Request]:
         toks, lps = handle.result()
+        if getattr(self.model, "tp_fused", None) is not None and self.num_steps % 16 == 0:
+            self._check_device_status()
         now = time.perf_counter()
         finished = self.scheduler.update(out, toks, lps, now=now)
         for req in finished:

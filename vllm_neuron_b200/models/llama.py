@@ -114,7 +114,7 @@ class LlamaForCausalLM(torch.nn.Module):
                                          cfg.rope_scaling, device=self.device)
         self.kv_caches: list[tuple[torch.Tensor, torch.Tensor]] = []
         self._alloc_workspace(max_tokens, max_decode_tokens, max_seqs)
-        self.tp_fused = None  # TPFusedComm: fused reduce-scatter / all-gather decode path
+        self.tp_fused = None  # TPFusedComm: fused all-reduce + residual + RMSNorm (decode)
 
     # ---------------------------------------------------------------- init / weights
     def _alloc_workspace(self, max_tokens, max_dec, max_seqs):
@@ -154,7 +154,7 @@ class LlamaForCausalLM(torch.nn.Module):
                 prm.normal_(0.0, std, generator=g)
 
     def enable_fused_comm(self, cpu_group=None):
-        """Use the fused GEMM + reduce-scatter / norm + all-gather kernels for TP decode."""
+        """Use the fused one-shot all-reduce + residual + RMSNorm kernel for TP decode."""
         if self.tp.world > 1 and self.device.type == "cuda":
             from ..parallel.fused import TPFusedComm
 
@@ -179,7 +179,7 @@ class LlamaForCausalLM(torch.nn.Module):
         fused = small and self.tp_fused is not None
         tp = self.tp
         res = self.ws_residual[:T]
-        x = self.tp_fused.x[:T] if fused else self.ws_x[:T]
+        x = self.ws_x[:T]
         ops.embedding(b.input_ids, self.embed, self.vocab_start, self.vocab_start + self.V_local, out=res,
                       last_tok=b.last_tok)
         tp.all_reduce_(res)
@@ -207,13 +207,10 @@ class LlamaForCausalLM(torch.nn.Module):
             attn = self.ws_attn[:T]
             self._attention(q, attn, k_cache, v_cache, b)
             nxt_norm = ly.post_norm
-            if fused:
-                x = self.tp_fused.rs_norm(attn, ly.o, res, nxt_norm, self.eps)
-            elif small:
+            if small:
                 acc = self.acc_h[:T]
                 L.gemm_accumulate(attn, ly.o, acc)
-                tp.all_reduce_(acc)
-                ops.add_rmsnorm(acc, res, nxt_norm, self.eps, out=x, clear_x=True)
+                self._allreduce_norm(acc, res, nxt_norm, x, fused)
             else:
                 h = L.gemm_out(attn, ly.o, out=self.ws_h[:T])
                 tp.all_reduce_(h)
@@ -224,13 +221,9 @@ class LlamaForCausalLM(torch.nn.Module):
                 acc = self.acc_gu[:T]
                 L.gemm_accumulate(x, ly.gate_up, acc)
                 act = ops.silu_mul(acc, out=self.ws_act[:T], blk=self.silu_blk, clear_input=True)
-                if fused:
-                    x = self.tp_fused.rs_norm(act, ly.down, res, nxt_norm, self.eps)
-                else:
-                    acc = self.acc_h[:T]
-                    L.gemm_accumulate(act, ly.down, acc)
-                    tp.all_reduce_(acc)
-                    ops.add_rmsnorm(acc, res, nxt_norm, self.eps, out=x, clear_x=True)
+                acc = self.acc_h[:T]
+                L.gemm_accumulate(act, ly.down, acc)
+                self._allreduce_norm(acc, res, nxt_norm, x, fused)
             else:
                 if self.silu_blk:
                     act = L.gemm_silu(x, ly.gate_up, out=self.ws_act[:T])
@@ -241,6 +234,14 @@ class LlamaForCausalLM(torch.nn.Module):
                 tp.all_reduce_(h)
                 ops.add_rmsnorm(h, res, nxt_norm, self.eps, out=x)
         return self.compute_logits(x, b.logits_indices)
+
+    def _allreduce_norm(self, acc, res, norm_w, x, fused: bool):
+        """Decode-size row-parallel epilogue: ``res += all_reduce(acc)``, ``x = rmsnorm(res)``."""
+        if fused:
+            self.tp_fused.allreduce_norm(acc, res, norm_w, self.eps, x)
+        else:
+            self.tp.all_reduce_(acc)
+            ops.add_rmsnorm(acc, res, norm_w, self.eps, out=x, clear_x=True)
 
     def _attention(self, q, attn, k_cache, v_cache, b: ForwardBatch, window: int = 0, sinks=None):
         T = b.num_tokens

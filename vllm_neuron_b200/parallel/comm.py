@@ -92,3 +92,44 @@ class GroupComm:
 
 
 SINGLE = GroupComm(None)
+
+
+class EmulatedRankComm(GroupComm):
+    """One rank's share of a TP group of ``world`` ranks, run alone on one device.
+
+    Shapes are sharded as for rank ``rank`` of ``world``, but every collective is local: an
+    all-reduce keeps the local partial, an all-gather tiles the local shard.  The numbers it
+    computes are not those of the real group; it exists so a single GPU can be profiled
+    (ncu launch lists, per-kernel timings) with exactly one rank's kernel shapes.
+    """
+
+    def __init__(self, world: int, rank: int = 0):
+        super().__init__(None)
+        self.world, self.rank = world, rank
+        self.ranks = list(range(world))
+
+    def all_reduce_(self, t):
+        return t
+
+    def all_gather(self, t, dim: int = 0, out=None):
+        res = torch.cat([t] * self.world, dim=dim)
+        if out is not None:
+            out.copy_(res)
+            return out
+        return res
+
+    def reduce_scatter(self, t, out=None):
+        part = t.chunk(self.world, 0)[self.rank]
+        if out is not None:
+            out.copy_(part)
+            return out
+        return part.contiguous()
+
+    def broadcast_(self, t, src: int = 0):
+        return t
+
+    def all_to_all(self, t, out=None):
+        if out is not None:
+            out.copy_(t)
+            return out
+        return t.clone()
