@@ -2,6 +2,7 @@
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
+#include <stdint.h>
 
 namespace b200 {
 
@@ -27,9 +28,20 @@ struct PagedAttnParams {
   int window;                    // 0 = full attention
   float scale_log2;              // softmax scale * log2(e)
   int total_tokens;
+  long long kv_rows;             // num_blocks * Hkv * block_size of one cache (0 = unknown)
+  uint32_t* status;              // device status word for bounded waits (may be null)
+  int* sched;                    // decode unit counters [2], zero between launches (may be null)
 };
 
 void paged_attention_launch(const PagedAttnParams& p, int num_work, int head_dim, bool decode,
                             cudaStream_t stream);
+
+// Persistent TMA-fed decode kernel (paged_decode.cu); used for decode batches when the caches
+// are contiguous [num_blocks, Hkv, block_size, D] tensors with block_size % 16 == 0 and a
+// unit counter is given.
+bool paged_decode_tma_supported(const PagedAttnParams& p, int head_dim);
+void paged_decode_tma_launch(const PagedAttnParams& p, int num_work, int head_dim,
+                             cudaStream_t stream);
+int paged_decode_warps_per_cta();
 
 }  // namespace b200

@@ -421,7 +421,9 @@ static void launch_attn(const PagedAttnParams& p, int num_work, cudaStream_t str
 void paged_attention_launch(const PagedAttnParams& p, int num_work, int head_dim, bool decode,
                             cudaStream_t stream) {
   if (num_work == 0) return;
-  if (head_dim == 128) {
+  if (decode && paged_decode_tma_supported(p, head_dim)) {
+    paged_decode_tma_launch(p, num_work, head_dim, stream);
+  } else if (head_dim == 128) {
     decode ? launch_attn<128, true>(p, num_work, stream)
            : launch_attn<128, false>(p, num_work, stream);
   } else if (head_dim == 64) {

@@ -37,6 +37,23 @@ uint32_t* status_word() {
   return p;
 }
 
+// Unit counters of the persistent decode attention kernel, one pair per device (zeroed once;
+// each launch's last warp resets them).
+int* decode_sched_words() {
+  static std::mutex mu;
+  static std::unordered_map<int, int*> words;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> g(mu);
+  auto it = words.find(dev);
+  if (it != words.end()) return it->second;
+  int* p = nullptr;
+  TORCH_CHECK(cudaMalloc(&p, 2 * sizeof(int)) == cudaSuccess, "decode counter allocation failed");
+  TORCH_CHECK(cudaMemset(p, 0, 2 * sizeof(int)) == cudaSuccess, "decode counter init failed");
+  words[dev] = p;
+  return p;
+}
+
 int64_t read_status() {
   uint32_t v = 0;
   TORCH_CHECK(cudaMemcpy(&v, status_word(), sizeof(v), cudaMemcpyDeviceToHost) == cudaSuccess);
@@ -136,6 +153,11 @@ void paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::T
   p.window = (int)window;
   p.scale_log2 = (float)(scale * 1.4426950408889634);
   p.total_tokens = (int)q.size(0);
+  p.status = status_word();
+  if (decode && k_cache.is_contiguous() && v_cache.is_contiguous()) {
+    p.kv_rows = k_cache.size(0) * k_cache.size(1) * k_cache.size(2);
+    p.sched = decode_sched_words();
+  }
   const int num_work = (int)work.size(0);
   b200::paged_attention_launch(p, num_work, D, decode, cur_stream());
   check_launch("paged_attention", num_work == 0 ? 0 : (num_splits > 1 ? 2 : 1));

@@ -95,6 +95,30 @@ def _make_batch(device, q_lens, ctx_lens, Hq, Hkv, D, bs=16, num_blocks=None, se
 
 
 @pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("bs", [16, 32])
+@pytest.mark.parametrize("q_len", [1, 3])
+@pytest.mark.parametrize("window,sinks", [(0, False), (100, True)])
+def test_paged_decode_tma(cuda_device, D, bs, q_len, window, sinks):
+    """Decode batches run the persistent TMA kernel (contiguous caches, block_size % 16 == 0);
+    several split factors, including splits that are empty for short sequences."""
+    Hq, Hkv = (16, 4) if D == 128 else (20, 4)
+    ctx = [1, 15, 16, 17, 63, 64, 65, 300, 1000, 2047, 5]
+    q_lens = [q_len] * len(ctx)
+    q, kc, vc, bt, sl, qs = _make_batch(cuda_device, q_lens, ctx, Hq, Hkv, D, bs=bs)
+    sink_t = (torch.randn(Hq, device=cuda_device) * 2).float() if sinks else None
+    scale = 1 / math.sqrt(D)
+    w = ops.build_work(np.array(q_lens), sl.cpu().numpy(), Hq // Hkv, Hkv)
+    assert w.decode
+    work = torch.from_numpy(w.work).to(cuda_device)
+    ref = ops.paged_attention_ref(q, kc, vc, bt, sl, qs, scale, window, sink_t)
+    for splits in sorted({1, w.num_splits, 5, 24}):
+        for _ in range(2):  # the unit counter must be reset between launches
+            out = ops.paged_attention(q, kc, vc, bt, sl, qs, work, True, splits, scale,
+                                      window=window, sinks=sink_t)
+            assert _rel_err(out, ref) < 2e-2, splits
+
+
+@pytest.mark.parametrize("D", [64, 128])
 @pytest.mark.parametrize("case", ["prefill", "decode", "mixed", "chunked"])
 @pytest.mark.parametrize("window,sinks", [(0, False), (128, True), (0, True)])
 def test_paged_attention(cuda_device, D, case, window, sinks):

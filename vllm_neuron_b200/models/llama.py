@@ -132,7 +132,7 @@ class LlamaForCausalLM(torch.nn.Module):
         self.acc_gu = torch.zeros(max_dec, 2 * self.I, dtype=torch.float32, device=d)
         self.ws_logits_x = torch.zeros(max_seqs, self.H, dtype=bf, device=d)
         self.ws_logits = torch.zeros(max_seqs, self.V_local, dtype=bf, device=d)
-        self.attn_splits_max = 16
+        self.attn_splits_max = 32
         self.ws_part_o = torch.zeros(self.attn_splits_max * max_dec * self.Hq * self.D,
                                      dtype=torch.float32, device=d)
         self.ws_part_lse = torch.zeros(self.attn_splits_max * max_dec * self.Hq,

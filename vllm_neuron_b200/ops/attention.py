@@ -25,6 +25,8 @@ from ._ext import ext
 PREFILL_ROWS = 64
 DECODE_ROWS = 16
 KV_TILE = 64
+DECODE_TILE = 16   # tokens per TMA tile of the decode kernel
+DECODE_WARPS = 8   # persistent warps per SM of the decode kernel
 
 
 @dataclass
@@ -34,13 +36,6 @@ class AttnWork:
     work: np.ndarray  # [W, 2] int32
     decode: bool
     num_splits: int
-
-
-def resident_ctas(head_dim: int, decode: bool = True) -> int:
-    """CTAs per SM allowed by shared memory (Q tile + double-buffered 64-token K/V tiles)."""
-    rows = DECODE_ROWS if decode else PREFILL_ROWS
-    smem = rows * head_dim * 2 + 4 * KV_TILE * head_dim * 2
-    return max(1, (227 * 1024) // (smem + 1024))
 
 
 def build_work(q_lens: np.ndarray, seq_lens: np.ndarray, group: int, num_kv_heads: int,
@@ -55,14 +50,14 @@ def build_work(q_lens: np.ndarray, seq_lens: np.ndarray, group: int, num_kv_head
     decode = bool(len(rows) > 0 and rows.max() <= DECODE_ROWS)
     if decode:
         work = np.stack([np.arange(len(rows)), np.zeros(len(rows), dtype=np.int64)], 1)
-        ctas = len(rows) * num_kv_heads
-        max_tiles = int(math.ceil(int(np.max(seq_lens)) / KV_TILE)) if len(rows) else 1
-        # Split the KV range until the grid spans several waves of resident CTAs (decode CTAs
-        # are memory-bound; a grid of ~1 wave loses up to half the bandwidth to the tail).
-        slots = num_sms * resident_ctas(head_dim)
-        splits = 1
-        while ctas * splits < 4 * slots and splits < max_splits and splits * 2 <= max(1, max_tiles // 2):
-            splits += 1
+        units = len(rows) * num_kv_heads
+        max_len = int(np.max(seq_lens)) if len(rows) else 1
+        # csrc/attn/paged_decode.cu: persistent warps (DECODE_WARPS per SM) claim
+        # (sequence, KV head, split) units.  Aim for ~3 units per warp for load balance, but
+        # keep at least 4 tiles (64 tokens) per split so the per-unit cost stays amortised.
+        warps = num_sms * DECODE_WARPS
+        splits = max(1, min(max_splits, math.ceil(3 * warps / max(1, units)),
+                            max(1, max_len // (4 * DECODE_TILE))))
         return AttnWork(work.astype(np.int32), True, splits)
     seqs, starts = [], []
     for b, r in enumerate(rows):
