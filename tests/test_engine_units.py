@@ -101,3 +101,21 @@ def test_parallel_group_math():
     assert kv == [[0, 4], [1, 5], [2, 6], [3, 7]] and head == [[0, 1, 2, 3], [4, 5, 6, 7]]
     with pytest.raises(ValueError):
         ps.ParallelConfig(world_size=8, tensor_parallel_size=3, data_parallel_size=1).validate()
+
+
+def test_emulated_rank_engine_runs_on_cpu():
+    """A single process can run one rank's share of TP=2 (profiling aid) without a process group."""
+    from vllm_neuron_b200.engine.llm_engine import EngineArgs, LLMEngine
+    from vllm_neuron_b200.engine.sampling_params import SamplingParams
+    from vllm_neuron_b200.parallel.comm import EmulatedRankComm
+
+    cfg = {"architectures": ["LlamaForCausalLM"], "model_type": "llama", "hidden_size": 64,
+           "num_hidden_layers": 1, "num_attention_heads": 4, "num_key_value_heads": 2, "head_dim": 16,
+           "intermediate_size": 128, "vocab_size": 256, "max_position_embeddings": 128}
+    eng = LLMEngine(EngineArgs(model=cfg, max_num_seqs=2, max_model_len=64, max_num_batched_tokens=64,
+                               load_format="dummy", device="cpu", num_gpu_blocks=32, dtype="float32"),
+                    tp=EmulatedRankComm(2))
+    assert eng.model.Hq == 2 and eng.model.Hkv == 1
+    eng.add_request(list(range(10)), SamplingParams(temperature=0.0, max_tokens=3, ignore_eos=True))
+    done = eng.run_until_done()
+    assert len(done) == 1 and len(done[0].output_token_ids) == 3

@@ -90,7 +90,8 @@ class LLMEngine:
             self.model.init_random(seed=args.seed)
         else:
             load_checkpoint_into(self.model, self.model_path)
-        if tp.world > 1 and self.device.type == "cuda" and self.b200_config.fused_comm:
+        real_group = tp.world > 1 and tp.group is not None
+        if real_group and self.device.type == "cuda" and self.b200_config.fused_comm:
             from ..parallel import state as ps
 
             self.model.enable_fused_comm(ps.get_parallel_state().cpu)
@@ -100,7 +101,7 @@ class LLMEngine:
                                   cuda_graphs=args.cuda_graphs and self.b200_config.cuda_graphs,
                                   device=self.device, seed=args.seed)
         nb = args.num_gpu_blocks or self.runner.profile_num_blocks(args.gpu_memory_utilization)
-        if tp.world > 1 and self.device.type == "cuda":
+        if real_group and self.device.type == "cuda":
             t = torch.tensor([nb], dtype=torch.int64, device=self.device)
             torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MIN, group=tp.group)
             nb = int(t.item())
