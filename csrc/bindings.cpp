@@ -13,6 +13,7 @@
 #include "comm/symm_mem.h"
 #include "gemm/gemm.h"
 #include "misc/misc.h"
+#include "moe/moe.h"
 
 namespace {
 
@@ -350,6 +351,130 @@ void tp_allreduce_norm(at::Tensor& acc, const std::vector<int64_t>& recv_ptrs,
   check_launch("tp_allreduce_norm", p.T > 0 ? 1 : 0);
 }
 
+// ------------------------------------------------------------------------------ MoE
+// out[rows of expert e] = x_perm[rows] @ w[e]^T for the tile list written by moe_align.
+// x_perm [R, K] bf16 (expert-sorted rows), w [E_local, N, K] bf16, out [R, N] (bf16) with the
+// EPI_BF16 or EPI_SILU_BF16 epilogue.
+void gemm_grouped(const at::Tensor& x_perm, const at::Tensor& w, at::Tensor& out,
+                  const at::Tensor& gtiles, const at::Tensor& gcount, int64_t epi, int64_t bn) {
+  CHECK_CUDA(x_perm);
+  CHECK_BF16(x_perm);
+  CHECK_BF16(w);
+  CHECK_BF16(out);
+  TORCH_CHECK(w.dim() == 3 && w.is_contiguous() && w.size(2) == x_perm.size(1), "gemm_grouped: w");
+  TORCH_CHECK(x_perm.stride(1) == 1 && out.stride(1) == 1, "gemm_grouped: inner dims");
+  TORCH_CHECK(gtiles.scalar_type() == at::kInt && gtiles.is_contiguous() && gtiles.size(-1) == 4,
+              "gemm_grouped: gtiles must be int32 [n, 4]");
+  TORCH_CHECK(epi == b200::EPI_BF16 || epi == b200::EPI_SILU_BF16, "gemm_grouped: epilogue");
+  const c10::cuda::CUDAGuard guard(x_perm.device());
+  b200::GemmArgs g{};
+  g.A = x_perm.data_ptr();
+  g.B = w.data_ptr();
+  g.out = out.data_ptr();
+  g.lda = x_perm.stride(0);
+  g.ldb = w.stride(1);
+  g.ldo = out.stride(0);
+  g.M = (int)x_perm.size(0);
+  g.N = (int)w.size(1);
+  g.K = (int)w.size(2);
+  g.bn = (int)bn;
+  g.epi = (int)epi;
+  g.splits = 1;
+  g.status = status_word();
+  g.gtiles = gtiles.data_ptr<int>();
+  g.gcount = gcount.data_ptr<int>();
+  g.gmax = (int)gtiles.size(0);
+  g.num_groups = (int)w.size(0);
+  b200::gemm_bf16_launch(g, cur_stream());
+  check_launch("gemm_grouped");
+}
+
+void moe_route(const at::Tensor& logits, c10::optional<at::Tensor> bias, int64_t k, int64_t mode,
+               bool renorm, at::Tensor& ids, at::Tensor& weights) {
+  CHECK_CUDA(logits);
+  CHECK_BF16(logits);
+  TORCH_CHECK(logits.stride(1) == 1, "moe_route: logits rows must be contiguous");
+  TORCH_CHECK(ids.scalar_type() == at::kInt && weights.scalar_type() == at::kFloat, "moe_route: out dtypes");
+  const c10::cuda::CUDAGuard guard(logits.device());
+  const float* b = nullptr;
+  if (bias.has_value()) {
+    TORCH_CHECK(bias->scalar_type() == at::kFloat, "moe_route: bias must be fp32");
+    b = bias->data_ptr<float>();
+  }
+  b200::moe_route_launch(reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()), logits.stride(0),
+                         b, (int)logits.size(0), (int)logits.size(1), (int)k, (int)mode, renorm,
+                         ids.data_ptr<int>(), weights.data_ptr<float>(), cur_stream());
+  check_launch("moe_route", logits.size(0) > 0 ? 1 : 0);
+}
+
+void moe_align(const at::Tensor& ids, int64_t e_start, int64_t e_local, at::Tensor& offsets,
+               at::Tensor& sorted_src, at::Tensor& row_expert, at::Tensor& inv_pos,
+               at::Tensor& gtiles, at::Tensor& gcount) {
+  CHECK_CUDA(ids);
+  TORCH_CHECK(ids.scalar_type() == at::kInt && ids.is_contiguous(), "moe_align: ids int32");
+  const c10::cuda::CUDAGuard guard(ids.device());
+  b200::moe_align_launch(ids.data_ptr<int>(), (int)ids.numel(), (int)e_start, (int)e_local,
+                         offsets.data_ptr<int>(), sorted_src.data_ptr<int>(),
+                         row_expert.data_ptr<int>(), inv_pos.data_ptr<int>(), gtiles.data_ptr<int>(),
+                         gcount.data_ptr<int>(), (int)gtiles.size(0), cur_stream());
+  check_launch("moe_align");
+}
+
+void moe_gather(const at::Tensor& x, const at::Tensor& sorted_src, int64_t topk,
+                const at::Tensor& offsets, at::Tensor& out) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  TORCH_CHECK(x.stride(1) == 1 && out.is_contiguous(), "moe_gather: layouts");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int e_local = (int)offsets.numel() - 1;
+  b200::moe_gather_launch(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0),
+                          sorted_src.data_ptr<int>(), (int)topk, offsets.data_ptr<int>() + e_local,
+                          (int)out.size(0), (int)x.size(1),
+                          reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), cur_stream());
+  check_launch("moe_gather", out.size(0) > 0 ? 1 : 0);
+}
+
+void moe_act(const at::Tensor& gu, c10::optional<at::Tensor> bias, const at::Tensor& row_expert,
+             const at::Tensor& offsets, int64_t mode, double alpha, double limit, at::Tensor& out) {
+  CHECK_CUDA(gu);
+  CHECK_BF16(gu);
+  TORCH_CHECK(gu.is_contiguous() && out.is_contiguous(), "moe_act: layouts");
+  const c10::cuda::CUDAGuard guard(gu.device());
+  const __nv_bfloat16* b = nullptr;
+  if (bias.has_value()) {
+    CHECK_BF16(*bias);
+    b = reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr());
+  }
+  const int e_local = (int)offsets.numel() - 1;
+  b200::moe_act_launch(reinterpret_cast<const __nv_bfloat16*>(gu.data_ptr()), b,
+                       row_expert.data_ptr<int>(), offsets.data_ptr<int>() + e_local,
+                       (int)out.size(0), (int)out.size(1), (int)mode, (float)alpha, (float)limit,
+                       reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), cur_stream());
+  check_launch("moe_act", out.size(0) > 0 ? 1 : 0);
+}
+
+void moe_combine(const at::Tensor& y, const at::Tensor& inv_pos, const at::Tensor& weights,
+                 const at::Tensor& ids, c10::optional<at::Tensor> bias, int64_t e_start,
+                 at::Tensor& out) {
+  CHECK_CUDA(y);
+  CHECK_BF16(y);
+  CHECK_BF16(out);
+  TORCH_CHECK(y.is_contiguous() && out.stride(1) == 1, "moe_combine: layouts");
+  const c10::cuda::CUDAGuard guard(y.device());
+  const __nv_bfloat16* b = nullptr;
+  if (bias.has_value()) {
+    CHECK_BF16(*bias);
+    b = reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr());
+  }
+  const int T = (int)out.size(0);
+  b200::moe_combine_launch(reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()), inv_pos.data_ptr<int>(),
+                           weights.data_ptr<float>(), ids.data_ptr<int>(), b, (int)e_start, T,
+                           (int)ids.size(1), (int)out.size(1),
+                           reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0),
+                           cur_stream());
+  check_launch("moe_combine", T > 0 ? 1 : 0);
+}
+
 int64_t num_sms() { return b200::num_sms_cached(); }
 int64_t launch_count() { return g_launches.load(); }
 
@@ -375,4 +500,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_free", &symm_free);
   m.def("tensor_from_ptr", &tensor_from_ptr);
   m.def("tp_allreduce_norm", &tp_allreduce_norm);
+  m.def("gemm_grouped", &gemm_grouped);
+  m.def("moe_route", &moe_route);
+  m.def("moe_align", &moe_align);
+  m.def("moe_gather", &moe_gather);
+  m.def("moe_act", &moe_act);
+  m.def("moe_combine", &moe_combine);
 }

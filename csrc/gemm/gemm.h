@@ -26,6 +26,12 @@ struct GemmArgs {
   int group_m;    // rasterization group along M (0 = default)
   int max_ctas;   // cap on persistent CTAs (0 = number of SMs)
   uint32_t* status;  // device status word for bounded-wait failures (may be null)
+  // Grouped (MoE) mode: B is [num_groups * N, K]; gtiles = int4 (group, first row, end row, -)
+  // entries written on the device, *gcount of them, at most gmax.
+  const int* gtiles = nullptr;
+  const int* gcount = nullptr;
+  int gmax = 0;
+  int num_groups = 0;
 };
 
 void gemm_bf16_launch(const GemmArgs& args, cudaStream_t stream);

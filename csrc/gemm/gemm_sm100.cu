@@ -19,6 +19,13 @@
 //   EPI_SILU_BF16 out[m, j] = silu(D[m, g]) * D[m, u] where the weight rows of each BN tile
 //                 are [BN/2 gate rows | BN/2 up rows] (interleaved at load time)
 //
+// Grouped mode (MoE experts): the A operand is the expert-sorted token rows and B stacks the
+// experts' weights [E * N, K].  A device tile list, written by the routing kernels, gives
+// per 128-row block (expert, first row, end row); the tile of (entry, nb) multiplies rows
+// [first, first + 128) of A by rows [expert * N + nb * BN, ...) of B and stores rows below the
+// entry's end row only.  Rows past the end of the block belong to the next expert (or are
+// TMA zero fill) and are discarded.
+//
 // This is the B200 replacement of the dense projections that the reference runs through
 // its NKI qkv / mlp / output_projection kernels (vllm_neuron/functional/attention/qkv.py:672,
 // vllm_neuron/functional/mlp.py:65, vllm_neuron/functional/attention/o_proj.py:124).
@@ -47,7 +54,32 @@ struct GemmParams {
   void* out;
   long long ldo;
   uint32_t* status;
+  // grouped mode
+  int grouped;
+  const int4* gtiles;  // [entries] (expert, first row, end row, unused)
+  const int* gcount;   // number of valid entries
 };
+
+// Row coordinates of tile `mb` (an m-block index, or a tile-list entry in grouped mode).
+struct TileRows {
+  int a_row;   // first row of the A tile
+  int b_base;  // row offset of the B operand (expert * N in grouped mode)
+  int m_lim;   // rows >= m_lim are not stored
+};
+__device__ __forceinline__ TileRows tile_rows(const GemmParams& p, int mb) {
+  TileRows t;
+  if (p.grouped) {
+    const int4 g = p.gtiles[mb];
+    t.a_row = g.y;
+    t.b_base = g.x * p.N;
+    t.m_lim = g.z;
+  } else {
+    t.a_row = mb * kBM;
+    t.b_base = 0;
+    t.m_lim = p.M;
+  }
+  return t;
+}
 
 __device__ __forceinline__ void decode_tile(const GemmParams& p, int tile, int& mb, int& nb,
                                             int& split) {
@@ -87,6 +119,15 @@ struct SegCursor {
       k1 = (int)min((long long)p.num_k_blocks, k0 + (u_end - u));
       u += k1 - k0;
       decode_tile(p, t, mb, nb, split);
+      return true;
+    }
+    if (p.grouped) {
+      if (tile >= *p.gcount * p.num_n_blocks) return false;
+      mb = tile / p.num_n_blocks;
+      nb = tile - mb * p.num_n_blocks;
+      k0 = 0;
+      k1 = p.num_k_blocks;
+      tile += gridDim.x;
       return true;
     }
     if (tile >= p.num_m_blocks * p.num_n_blocks * p.splits) return false;
@@ -164,11 +205,15 @@ __global__ void __launch_bounds__(192, 1)
       const uint64_t hint_b = kWeightIsA ? policy_evict_last()   // B = activations, reused
                                          : policy_evict_first();
       auto load_a = [&](int s, int kb, int mb) {
-        tma_load_2d(&tmA, &full_bar[s], smA + s * kATileBytes, kb * kBK, mb * kBM, hint_a);
+        tma_load_2d(&tmA, &full_bar[s], smA + s * kATileBytes, kb * kBK, tile_rows(p, mb).a_row,
+                    hint_a);
       };
-      auto load_b = [&](int s, int kb, int nb) {
-        tma_load_2d(&tmB, &full_bar[s], smB + s * kBTileBytes, kb * kBK, nb * BN, hint_b);
+      auto load_b = [&](int s, int kb, int nb, int mb) {
+        const int base = p.grouped ? tile_rows(p, mb).b_base : 0;
+        tma_load_2d(&tmB, &full_bar[s], smB + s * kBTileBytes, kb * kBK, base + nb * BN, hint_b);
       };
+      // The grouped tile list is written by the previous kernel.
+      if (p.grouped) pdl_wait();
       uint32_t it = 0;
       bool ok = true;
       SegCursor cur(p);
@@ -183,7 +228,7 @@ __global__ void __launch_bounds__(192, 1)
       for (int i = 0; i < STAGES; ++i) {
         if (have) {
           mbar_arrive_expect_tx(&full_bar[i], kStageBytes);
-          if (kWeightIsA) load_a(i, kb, mb); else load_b(i, kb, nb);
+          if (kWeightIsA) load_a(i, kb, mb); else load_b(i, kb, nb, mb);
           pre_mb[i] = mb;
           pre_nb[i] = nb;
           pre_kb[i] = kb;
@@ -199,7 +244,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
       for (int i = 0; i < STAGES; ++i) {
         if (i < npre) {
-          if (kWeightIsA) load_b(i, pre_kb[i], pre_nb[i]); else load_a(i, pre_kb[i], pre_mb[i]);
+          if (kWeightIsA) load_b(i, pre_kb[i], pre_nb[i], pre_mb[i]); else load_a(i, pre_kb[i], pre_mb[i]);
         }
       }
       // Phase 2: steady state.
@@ -212,7 +257,7 @@ __global__ void __launch_bounds__(192, 1)
         }
         mbar_arrive_expect_tx(&full_bar[s], kStageBytes);
         load_a(s, kb, mb);
-        load_b(s, kb, nb);
+        load_b(s, kb, nb, mb);
         ++it;
         if (++kb == k1) {
           have = cur.next(p, mb, nb, k0, k1);
@@ -231,6 +276,7 @@ __global__ void __launch_bounds__(192, 1)
   } else if (warp == 1) {
     // ------------------------------ MMA issuer ------------------------------
     if (elect_one()) {
+      if (p.grouped) pdl_wait();  // the tile list is written by the previous kernel
       uint32_t it = 0;
       int t_local = 0;
       bool ok = true;
@@ -279,7 +325,9 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t aph = (t_local >> 1) & 1;
       if (!mbar_wait_abortable(&tfull_bar[acc], aph, kTimeoutTmemFull, p.status, abort_flag)) break;
       tc_fence_after();
-      const int m = mb * kBM + row;
+      const TileRows trows = tile_rows(p, mb);
+      const int m = trows.a_row + row;
+      const int m_lim = trows.m_lim;
       const int n_base = nb * BN;
       const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
 
@@ -294,7 +342,7 @@ __global__ void __launch_bounds__(192, 1)
           tmem_ld_32x32b_x16(t_row + c, g);
           tmem_ld_32x32b_x16(t_row + H + c, u);
           tmem_ld_wait();
-          if (m < p.M) {
+          if (m < m_lim) {
             __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + (long long)m * p.ldo;
             uint32_t packed[8];
 #pragma unroll
@@ -326,7 +374,7 @@ __global__ void __launch_bounds__(192, 1)
           tmem_ld_wait();
           const int n0 = n_base + c;
           if constexpr (EPI == EPI_BF16) {
-            if (m < p.M) {
+            if (m < m_lim) {
               __nv_bfloat16* o =
                   reinterpret_cast<__nv_bfloat16*>(p.out) + (long long)m * p.ldo + n0;
               if (n0 + 32 <= p.N && (p.ldo % 8) == 0) {
@@ -345,7 +393,7 @@ __global__ void __launch_bounds__(192, 1)
               }
             }
           } else if constexpr (EPI == EPI_BF16_T) {
-            if (m < p.M) {
+            if (m < m_lim) {
               __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + m;
 #pragma unroll
               for (int j = 0; j < 32; ++j)
@@ -353,7 +401,7 @@ __global__ void __launch_bounds__(192, 1)
                   o[(long long)(n0 + j) * p.ldo] = __float2bfloat16(__uint_as_float(r[j]));
             }
           } else if constexpr (EPI == EPI_F32_RED) {
-            if (m < p.M) {
+            if (m < m_lim) {
               float* o = reinterpret_cast<float*>(p.out) + (long long)m * p.ldo + n0;
               if (n0 + 32 <= p.N && (p.ldo % 4) == 0) {
 #pragma unroll
@@ -368,7 +416,7 @@ __global__ void __launch_bounds__(192, 1)
               }
             }
           } else {  // EPI_F32_RED_T: fp32 reductions into out[n, m]
-            if (m < p.M) {
+            if (m < m_lim) {
               float* o = reinterpret_cast<float*>(p.out) + m;
 #pragma unroll
               for (int j = 0; j < 32; ++j)
@@ -451,9 +499,16 @@ void gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
   if (a.lda % 8 != 0 || a.ldb % 8 != 0)
     throw std::invalid_argument("gemm: row pitches must be multiples of 8 elements");
   const int bn = a.bn;
+  const bool grouped = a.gtiles != nullptr;
+  if (grouped && (a.splits > 1 || a.splits < 0 || a.num_groups < 1 || a.gmax < 1))
+    throw std::invalid_argument("gemm: grouped mode needs splits == 1, groups and a tile bound");
   const CUtensorMap ta = make_tmap_bf16_2d(a.A, a.K, a.M, a.lda, kBK, kBM, true);
-  const CUtensorMap tb = make_tmap_bf16_2d(a.B, a.K, a.N, a.ldb, kBK, bn, true);
+  const CUtensorMap tb = make_tmap_bf16_2d(a.B, a.K, grouped ? (uint64_t)a.N * a.num_groups : a.N,
+                                           a.ldb, kBK, bn, true);
   GemmParams p;
+  p.grouped = grouped ? 1 : 0;
+  p.gtiles = reinterpret_cast<const int4*>(a.gtiles);
+  p.gcount = a.gcount;
   p.M = a.M;
   p.N = a.N;
   p.K = a.K;
@@ -472,7 +527,8 @@ void gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
   p.out = a.out;
   p.ldo = a.ldo;
   p.status = a.status;
-  const long long tiles = (long long)p.num_m_blocks * p.num_n_blocks * p.splits;
+  const long long tiles = grouped ? (long long)a.gmax * p.num_n_blocks
+                                  : (long long)p.num_m_blocks * p.num_n_blocks * p.splits;
   int grid = num_sms_cached();
   if (a.max_ctas > 0 && a.max_ctas < grid) grid = a.max_ctas;
   if (p.streamk) {

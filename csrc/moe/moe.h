@@ -1,0 +1,40 @@
+// Host interface of the mixture-of-experts routing kernels (moe.cu).
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace b200 {
+
+enum RouteMode : int {
+  ROUTE_TOPK_SOFTMAX = 0,  // top-k of the logits, softmax over the k selected (GPT-OSS)
+  ROUTE_SOFTMAX_TOPK = 1,  // softmax over all experts, top-k, optional renormalisation (Qwen)
+  ROUTE_SIGMOID_TOPK = 2,  // sigmoid scores, top-k, optional renormalisation
+};
+
+enum MoeAct : int {
+  MOE_ACT_SILU = 0,    // silu(gate) * up
+  MOE_ACT_GPTOSS = 1,  // gate = min(gate, limit); up = clamp(up, +-limit);
+                       // (up + 1) * gate * sigmoid(alpha * gate)
+};
+
+void moe_route_launch(const __nv_bfloat16* logits, long long ld, const float* bias, int T, int E,
+                      int k, int mode, bool renorm, int* ids, float* weights, cudaStream_t s);
+
+// Groups the T*k assignments by local expert [e_start, e_start + e_local).
+void moe_align_launch(const int* ids, int n_assign, int e_start, int e_local, int* offsets,
+                      int* sorted_src, int* row_expert, int* inv_pos, int* gtiles, int* gcount,
+                      int gmax, cudaStream_t s);
+
+void moe_gather_launch(const __nv_bfloat16* x, long long ldx, const int* sorted_src, int topk,
+                       const int* total, int rows_cap, int H, __nv_bfloat16* out, cudaStream_t s);
+
+void moe_act_launch(const __nv_bfloat16* gu, const __nv_bfloat16* bias, const int* row_expert,
+                    const int* total, int rows_cap, int I, int mode, float alpha, float limit,
+                    __nv_bfloat16* out, cudaStream_t s);
+
+void moe_combine_launch(const __nv_bfloat16* y, const int* inv_pos, const float* weights,
+                        const int* ids, const __nv_bfloat16* bias, int e_start, int T, int k,
+                        int H, __nv_bfloat16* out, long long ldo, cudaStream_t s);
+
+}  // namespace b200

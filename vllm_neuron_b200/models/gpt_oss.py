@@ -1,0 +1,109 @@
+"""GPT-OSS (``GptOssForCausalLM``): alternating sliding-window (128) / full attention with learned
+per-head sinks, QKV and output biases, YaRN RoPE, and a mixture-of-experts MLP (top-k softmax
+routing with a router bias, clamped SwiGLU with alpha, per-expert biases).
+
+Attention runs on the dense decoder path of :mod:`.llama` (the paged attention kernel takes
+the layer's window and sinks).  The MLP is :func:`vllm_neuron_b200.ops.moe.moe_block`.  Experts
+are sharded across the tensor-parallel ranks (expert parallelism over the TP group): rank r
+holds experts ``[r * E/W, (r + 1) * E/W)``, computes their contribution for every token and
+the partial outputs are summed by the all-reduce that also serves attention-TP.
+
+MXFP4 checkpoints (``*_blocks`` uint8 nibbles + ``*_scales`` e8m0 per 32 elements) are
+dequantized to bf16 when loaded (:func:`dequant_mxfp4`).
+
+Reference: vllm_neuron/model/gpt_oss/model_bf16.py (attention with sinks :393,721,770,938,
+YaRN :142-232, MoE :982-1443), model_mxfp4.py and weight_loaders_mxfp4.py.
+"""
+from __future__ import annotations
+
+import torch
+
+from .. import ops
+from ..ops import moe as M
+from .llama import LlamaForCausalLM
+
+# e2m1 code points (sign bit 3, exponent bits 2-1, mantissa bit 0)
+_FP4_VALUES = [0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0, -0.0, -0.5, -1.0, -1.5, -2.0, -3.0, -4.0, -6.0]
+
+
+def dequant_mxfp4(blocks: torch.Tensor, scales: torch.Tensor, dtype=torch.bfloat16) -> torch.Tensor:
+    """``blocks [..., G, 16]`` uint8 (two e2m1 values per byte, low nibble first) and
+    ``scales [..., G]`` uint8 (e8m0, bias 127) -> ``[..., G * 32]``."""
+    lut = torch.tensor(_FP4_VALUES, dtype=torch.float32)
+    b = blocks.to(torch.int64)
+    lo = lut[b & 0x0F]
+    hi = lut[b >> 4]
+    v = torch.stack([lo, hi], dim=-1).reshape(*blocks.shape[:-1], 32)
+    e = scales.to(torch.int32) - 127
+    v = v * torch.pow(2.0, e.to(torch.float32))[..., None]
+    return v.reshape(*blocks.shape[:-2], blocks.shape[-2] * 32).to(dtype)
+
+
+def quant_mxfp4(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Round ``w [..., K]`` (K % 32 == 0) to MXFP4: returns ``(blocks [..., K/32, 16], scales)``.
+    Used to build random MXFP4 experts with the checkpoint format."""
+    lut = torch.tensor(_FP4_VALUES[:8], dtype=torch.float32)
+    x = w.float().reshape(*w.shape[:-1], w.shape[-1] // 32, 32)
+    amax = x.abs().amax(-1).clamp_min(1e-30)
+    e = torch.clamp(torch.ceil(torch.log2(amax / 6.0)), -127, 127)
+    scaled = x / torch.pow(2.0, e)[..., None]
+    mag = scaled.abs().clamp(max=6.0)
+    idx = (mag[..., None] - lut).abs().argmin(-1)
+    code = idx | ((scaled < 0).to(torch.int64) << 3)
+    code = code.reshape(*code.shape[:-1], 16, 2)
+    blocks = (code[..., 0] | (code[..., 1] << 4)).to(torch.uint8)
+    return blocks, (e + 127).to(torch.uint8)
+
+
+class GptOssForCausalLM(LlamaForCausalLM):
+    def __init__(self, cfg, *args, **kw):
+        W = kw.get("tp").world if kw.get("tp") is not None else 1
+        self.E = cfg.num_experts
+        self.topk = cfg.num_experts_per_tok
+        assert self.E % W == 0, f"{self.E} experts not divisible by TP={W}"
+        self.e_local = self.E // W
+        self.I_moe = cfg.intermediate_size
+        super().__init__(cfg, *args, **kw)
+        self.e_start = self.tp.rank * self.e_local
+        p = lambda *s: torch.nn.Parameter(torch.empty(*s, dtype=self.dtype, device=self.device),
+                                          requires_grad=False)
+        for ly in self.layers:
+            ly.o_bias = p(self.H)
+            ly.sinks = torch.nn.Parameter(torch.zeros(self.Hq, dtype=torch.float32, device=self.device),
+                                          requires_grad=False)
+        self.moe_ws = None
+        if self.device.type == "cuda":
+            self.moe_ws = M.MoEWorkspace.create(self.max_tokens, self.topk, self.E, self.e_local, self.H,
+                                                self.I_moe, self.device)
+
+    def _make_mlp(self, m, p, layer: int):
+        m.router = p(self.E, self.H)
+        m.router_bias = torch.nn.Parameter(torch.zeros(self.E, dtype=torch.float32, device=self.device),
+                                           requires_grad=False)
+        m.w_gu = p(self.e_local, 2 * self.I_moe, self.H)
+        m.b_gu = p(self.e_local, 2 * self.I_moe)
+        m.w_down = p(self.e_local, self.H, self.I_moe)
+        m.b_down = p(self.e_local, self.H)
+
+    def _mlp(self, i, ly, x, res, nxt_norm, T, small, fused):
+        h = self.ws_h[:T]
+        M.moe_block(x, ly.router, ly.w_gu, ly.w_down, self.topk, M.ROUTE_TOPK_SOFTMAX,
+                    router_b=ly.router_bias, b_gu=ly.b_gu,
+                    b_down=ly.b_down,  # each assignment is computed on exactly one rank
+                    act=M.ACT_GPTOSS, alpha=self.cfg.swiglu_alpha, limit=self.cfg.swiglu_limit,
+                    e_start=self.e_start, ws=self.moe_ws, out=h)
+        self.tp.all_reduce_(h)
+        ops.add_rmsnorm(h, res, nxt_norm, self.eps, out=x)
+
+    @torch.no_grad()
+    def init_random(self, seed: int = 0, std: float = 0.02):
+        super().init_random(seed, std)
+        g = torch.Generator(device=self.device)
+        g.manual_seed(seed * 1000 + 7 + self.tp.rank)
+        for ly in self.layers:
+            ly.sinks.normal_(0.0, 1.0, generator=g)
+
+    def load_hf_state_dict(self, get_tensor, names: set[str]):
+        from ..utils.weight_loader import load_gpt_oss
+
+        load_gpt_oss(self, get_tensor, names)

@@ -100,8 +100,10 @@ class LlamaForCausalLM(torch.nn.Module):
             m.qkv = p(qkv_out, self.H)
             m.qkv_bias = p(qkv_out) if cfg.attention_bias else None
             m.o = p(self.H, self.Hq * self.D)
-            m.gate_up = p(2 * self.I, self.H)
-            m.down = p(self.H, self.I)
+            m.o_bias = None
+            m.window = cfg.sliding_window if cfg.layer_is_sliding(len(self.layers)) else 0
+            m.sinks = None
+            self._make_mlp(m, p, len(self.layers))
             if cfg.qk_norm:
                 m.q_norm = p(self.D)
                 m.k_norm = p(self.D)
@@ -117,6 +119,11 @@ class LlamaForCausalLM(torch.nn.Module):
         self.tp_fused = None  # TPFusedComm: fused all-reduce + residual + RMSNorm (decode)
 
     # ---------------------------------------------------------------- init / weights
+    def _make_mlp(self, m, p, layer: int):
+        """Dense SwiGLU MLP parameters of one layer (MoE models override this)."""
+        m.gate_up = p(2 * self.I, self.H)
+        m.down = p(self.H, self.I)
+
     def _alloc_workspace(self, max_tokens, max_dec, max_seqs):
         d, bf = self.device, self.dtype
         self.ws_residual = torch.zeros(max_tokens, self.H, dtype=bf, device=d)
@@ -205,35 +212,43 @@ class LlamaForCausalLM(torch.nn.Module):
                                   k_cache, v_cache, b.slot_mapping, ly.q_norm, ly.k_norm, self.eps,
                                   rot_dim=self.cfg.rot_dim)
             attn = self.ws_attn[:T]
-            self._attention(q, attn, k_cache, v_cache, b)
+            self._attention(q, attn, k_cache, v_cache, b, window=ly.window, sinks=ly.sinks)
             nxt_norm = ly.post_norm
             if small:
                 acc = self.acc_h[:T]
                 L.gemm_accumulate(attn, ly.o, acc)
+                if ly.o_bias is not None and tp.rank == 0:
+                    acc.add_(ly.o_bias.float())
                 self._allreduce_norm(acc, res, nxt_norm, x, fused)
             else:
                 h = L.gemm_out(attn, ly.o, out=self.ws_h[:T])
+                if ly.o_bias is not None and tp.rank == 0:
+                    h.add_(ly.o_bias)
                 tp.all_reduce_(h)
                 ops.add_rmsnorm(h, res, nxt_norm, self.eps, out=x)
             # ---- MLP
             nxt_norm = self.layers[i + 1].input_norm if i + 1 < nL else self.final_norm
-            if small:
-                acc = self.acc_gu[:T]
-                L.gemm_accumulate(x, ly.gate_up, acc)
-                act = ops.silu_mul(acc, out=self.ws_act[:T], blk=self.silu_blk, clear_input=True)
-                acc = self.acc_h[:T]
-                L.gemm_accumulate(act, ly.down, acc)
-                self._allreduce_norm(acc, res, nxt_norm, x, fused)
-            else:
-                if self.silu_blk:
-                    act = L.gemm_silu(x, ly.gate_up, out=self.ws_act[:T])
-                else:
-                    gu = L.gemm_out(x, ly.gate_up)
-                    act = ops.silu_mul(gu, out=self.ws_act[:T])
-                h = L.gemm_out(act, ly.down, out=self.ws_h[:T])
-                tp.all_reduce_(h)
-                ops.add_rmsnorm(h, res, nxt_norm, self.eps, out=x)
+            self._mlp(i, ly, x, res, nxt_norm, T, small, fused)
         return self.compute_logits(x, b.logits_indices)
+
+    def _mlp(self, i: int, ly, x, res, nxt_norm, T: int, small: bool, fused: bool):
+        """Dense SwiGLU MLP; leaves ``x = nxt_norm(res += mlp(x))``."""
+        if small:
+            acc = self.acc_gu[:T]
+            L.gemm_accumulate(x, ly.gate_up, acc)
+            act = ops.silu_mul(acc, out=self.ws_act[:T], blk=self.silu_blk, clear_input=True)
+            acc = self.acc_h[:T]
+            L.gemm_accumulate(act, ly.down, acc)
+            self._allreduce_norm(acc, res, nxt_norm, x, fused)
+        else:
+            if self.silu_blk:
+                act = L.gemm_silu(x, ly.gate_up, out=self.ws_act[:T])
+            else:
+                gu = L.gemm_out(x, ly.gate_up)
+                act = ops.silu_mul(gu, out=self.ws_act[:T])
+            h = L.gemm_out(act, ly.down, out=self.ws_h[:T])
+            self.tp.all_reduce_(h)
+            ops.add_rmsnorm(h, res, nxt_norm, self.eps, out=x)
 
     def _allreduce_norm(self, acc, res, norm_w, x, fused: bool):
         """Decode-size row-parallel epilogue: ``res += all_reduce(acc)``, ``x = rmsnorm(res)``."""

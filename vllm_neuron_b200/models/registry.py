@@ -8,6 +8,7 @@ _MODELS = {
     "MistralForCausalLM": ("vllm_neuron_b200.models.llama", "LlamaForCausalLM"),
     "Qwen3ForCausalLM": ("vllm_neuron_b200.models.llama", "LlamaForCausalLM"),
     "Qwen2ForCausalLM": ("vllm_neuron_b200.models.llama", "LlamaForCausalLM"),
+    "GptOssForCausalLM": ("vllm_neuron_b200.models.gpt_oss", "GptOssForCausalLM"),
 }
 
 

@@ -10,6 +10,7 @@ from .linear import (gemm_accumulate, gemm_out, gemm_silu, gemm_skinny_bf16,
                      interleave_gate_up, silu_mul_ref)
 from .norm import add_rmsnorm, rmsnorm, rmsnorm_ref
 from .rope import cos_sin_table, rope_kv_write, rope_kv_write_ref
+from . import moe
 from .sampling import argmax, sample, sample_ref
 
 __all__ = [

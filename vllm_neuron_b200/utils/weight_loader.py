@@ -88,3 +88,62 @@ def load_dense_decoder(model, get_tensor: Callable[[str], torch.Tensor], names: 
     if not cfg.tie_word_embeddings:
         head = "lm_head.weight"
         _copy(model.lm_head, shard_rows(get_tensor(head), W, r, model.V_local), "lm_head")
+
+
+def _expert_tensor(get_tensor, names, base: str) -> torch.Tensor:
+    """An expert weight in bf16 form: ``base`` itself, or ``base_blocks`` + ``base_scales``
+    (MXFP4) dequantized."""
+    if base in names:
+        return get_tensor(base)
+    from ..models.gpt_oss import dequant_mxfp4
+
+    return dequant_mxfp4(get_tensor(base + "_blocks"), get_tensor(base + "_scales"))
+
+
+@torch.no_grad()
+def load_gpt_oss(model, get_tensor: Callable[[str], torch.Tensor], names: set[str]):
+    """GPT-OSS: attention as the dense decoder (plus sinks and o_proj bias), experts sharded by
+    expert index over the TP ranks.  HF stores ``gate_up_proj [E, H, 2I]`` with gate/up
+    interleaved in the last dim and ``down_proj [E, I, H]``; MXFP4 checkpoints store the
+    ``[E, 2I, H]`` / ``[E, H, I]`` (out, in) matrices as blocks + scales."""
+    cfg = model.cfg
+    W, r = model.tp.world, model.tp.rank
+    pre = "model."
+    _copy(model.embed, shard_rows(get_tensor(pre + "embed_tokens.weight"), W, r, model.V_local), "embed")
+    e0, el = model.e_start, model.e_local
+    for i, ly in enumerate(model.layers):
+        p = f"{pre}layers.{i}."
+        _copy(ly.input_norm, get_tensor(p + "input_layernorm.weight"), p + "input_layernorm")
+        _copy(ly.post_norm, get_tensor(p + "post_attention_layernorm.weight"), p + "post_attention_layernorm")
+        q = get_tensor(p + "self_attn.q_proj.weight")
+        k = get_tensor(p + "self_attn.k_proj.weight")
+        v = get_tensor(p + "self_attn.v_proj.weight")
+        _copy(ly.qkv, fused_qkv(q, k, v, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, W, r), p + "qkv")
+        qb = get_tensor(p + "self_attn.q_proj.bias")[:, None]
+        kb = get_tensor(p + "self_attn.k_proj.bias")[:, None]
+        vb = get_tensor(p + "self_attn.v_proj.bias")[:, None]
+        _copy(ly.qkv_bias, fused_qkv(qb, kb, vb, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, W, r)[:, 0],
+              p + "qkv_bias")
+        _copy(ly.o, shard_cols(get_tensor(p + "self_attn.o_proj.weight"), W, r), p + "o_proj")
+        _copy(ly.o_bias, get_tensor(p + "self_attn.o_proj.bias"), p + "o_proj.bias")
+        sinks = get_tensor(p + "self_attn.sinks").float()
+        _copy(ly.sinks, sinks[r * model.Hq:(r + 1) * model.Hq], p + "sinks")
+        _copy(ly.router, get_tensor(p + "mlp.router.weight"), p + "router")
+        _copy(ly.router_bias, get_tensor(p + "mlp.router.bias").float(), p + "router.bias")
+        gu_name = p + "mlp.experts.gate_up_proj"
+        if gu_name in names:
+            gu = get_tensor(gu_name)[e0:e0 + el].transpose(1, 2)   # [el, 2I, H] interleaved rows
+        else:
+            gu = _expert_tensor(get_tensor, names, gu_name)[e0:e0 + el]
+        gub = get_tensor(gu_name + "_bias")[e0:e0 + el]
+        _copy(ly.w_gu, torch.cat([gu[:, 0::2], gu[:, 1::2]], 1), p + "w_gu")
+        _copy(ly.b_gu, torch.cat([gub[:, 0::2], gub[:, 1::2]], 1), p + "b_gu")
+        dn_name = p + "mlp.experts.down_proj"
+        if dn_name in names:
+            dn = get_tensor(dn_name)[e0:e0 + el].transpose(1, 2)   # [el, H, I]
+        else:
+            dn = _expert_tensor(get_tensor, names, dn_name)[e0:e0 + el]
+        _copy(ly.w_down, dn, p + "w_down")
+        _copy(ly.b_down, get_tensor(dn_name + "_bias")[e0:e0 + el], p + "b_down")
+    _copy(model.final_norm, get_tensor(pre + "norm.weight"), "norm")
+    _copy(model.lm_head, shard_rows(get_tensor("lm_head.weight"), W, r, model.V_local), "lm_head")
