@@ -389,8 +389,9 @@ void gemm_grouped(const at::Tensor& x_perm, const at::Tensor& w, at::Tensor& out
   check_launch("gemm_grouped");
 }
 
-void moe_route(const at::Tensor& logits, c10::optional<at::Tensor> bias, int64_t k, int64_t mode,
-               bool renorm, at::Tensor& ids, at::Tensor& weights) {
+void moe_route(const at::Tensor& logits, c10::optional<at::Tensor> bias, int64_t num_experts,
+               int64_t k, int64_t mode, bool renorm, at::Tensor& ids, at::Tensor& weights,
+               c10::optional<at::Tensor> shared_gate) {
   CHECK_CUDA(logits);
   CHECK_BF16(logits);
   TORCH_CHECK(logits.stride(1) == 1, "moe_route: logits rows must be contiguous");
@@ -402,8 +403,10 @@ void moe_route(const at::Tensor& logits, c10::optional<at::Tensor> bias, int64_t
     b = bias->data_ptr<float>();
   }
   b200::moe_route_launch(reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()), logits.stride(0),
-                         b, (int)logits.size(0), (int)logits.size(1), (int)k, (int)mode, renorm,
-                         ids.data_ptr<int>(), weights.data_ptr<float>(), cur_stream());
+                         b, (int)logits.size(0), (int)num_experts, (int)k, (int)mode, renorm,
+                         ids.data_ptr<int>(), weights.data_ptr<float>(),
+                         shared_gate.has_value() ? shared_gate->data_ptr<float>() : nullptr,
+                         cur_stream());
   check_launch("moe_route", logits.size(0) > 0 ? 1 : 0);
 }
 
@@ -455,6 +458,7 @@ void moe_act(const at::Tensor& gu, c10::optional<at::Tensor> bias, const at::Ten
 
 void moe_combine(const at::Tensor& y, const at::Tensor& inv_pos, const at::Tensor& weights,
                  const at::Tensor& ids, c10::optional<at::Tensor> bias, int64_t e_start,
+                 c10::optional<at::Tensor> shared, c10::optional<at::Tensor> shared_gate,
                  at::Tensor& out) {
   CHECK_CUDA(y);
   CHECK_BF16(y);
@@ -470,6 +474,9 @@ void moe_combine(const at::Tensor& y, const at::Tensor& inv_pos, const at::Tenso
   b200::moe_combine_launch(reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()), inv_pos.data_ptr<int>(),
                            weights.data_ptr<float>(), ids.data_ptr<int>(), b, (int)e_start, T,
                            (int)ids.size(1), (int)out.size(1),
+                           shared.has_value() ? reinterpret_cast<const __nv_bfloat16*>(shared->data_ptr()) : nullptr,
+                           shared.has_value() ? shared->stride(0) : 0,
+                           shared_gate.has_value() ? shared_gate->data_ptr<float>() : nullptr,
                            reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0),
                            cur_stream());
   check_launch("moe_combine", T > 0 ? 1 : 0);

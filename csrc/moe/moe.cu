@@ -13,8 +13,9 @@
 //   gather   copies each assignment's token row into its expert-sorted row.
 //   act      SwiGLU of the expert gate/up projection (plain SiLU or GPT-OSS clamped form with
 //            alpha), per-expert bias.
-//   combine  out[t] = sum_j w[t, j] * (y[row(t, j)] + bias[e(t, j)]) in j order (the
-//            reference's topk_reduce, vllm_neuron/functional/moe/topk_reduce.py:28).
+//   combine  out[t] = g[t] * shared[t] + sum_j w[t, j] * (y[row(t, j)] + bias[e(t, j)]) in
+//            j order (the reference's topk_reduce, vllm_neuron/functional/moe/topk_reduce.py:28;
+//            shared is the optional shared expert, g its sigmoid gate from the router).
 #include <cuda_bf16.h>
 
 #include <stdexcept>
@@ -30,13 +31,17 @@ constexpr int kMaxExpertsPerLane = 16;  // E <= 512
 
 __global__ void moe_route_kernel(const __nv_bfloat16* __restrict__ logits, long long ld,
                                  const float* __restrict__ bias, int T, int E, int k, int mode,
-                                 int renorm, int* __restrict__ ids, float* __restrict__ weights) {
+                                 int renorm, int* __restrict__ ids, float* __restrict__ weights,
+                                 float* __restrict__ shared_gate) {
   pdl_trigger();
   pdl_wait();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= T) return;
   const __nv_bfloat16* row = logits + (long long)warp * ld;
+  // column E (when present) is the shared expert's gate logit
+  if (shared_gate != nullptr && lane == 0)
+    shared_gate[warp] = 1.f / (1.f + __expf(-__bfloat162float(row[E])));
   float v[kMaxExpertsPerLane];
 #pragma unroll
   for (int i = 0; i < kMaxExpertsPerLane; ++i) {
@@ -223,12 +228,16 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y,
                                    const int* __restrict__ inv_pos,
                                    const float* __restrict__ weights, const int* __restrict__ ids,
                                    const __nv_bfloat16* __restrict__ bias, int e_start, int k,
-                                   int H, __nv_bfloat16* __restrict__ out, long long ldo) {
+                                   int H, const __nv_bfloat16* __restrict__ shared,
+                                   long long ld_shared, const float* __restrict__ shared_gate,
+                                   __nv_bfloat16* __restrict__ out, long long ldo) {
   pdl_trigger();
   pdl_wait();
   const int t = blockIdx.x;
+  const float sg = shared != nullptr ? (shared_gate != nullptr ? shared_gate[t] : 1.f) : 0.f;
   for (int c = threadIdx.x; c < H; c += blockDim.x) {
     float acc = 0.f;
+    if (shared != nullptr) acc = sg * __bfloat162float(shared[(long long)t * ld_shared + c]);
     for (int j = 0; j < k; ++j) {
       const int pos = inv_pos[(long long)t * k + j];
       if (pos < 0) continue;
@@ -244,14 +253,15 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y,
 }
 
 void moe_route_launch(const __nv_bfloat16* logits, long long ld, const float* bias, int T, int E,
-                      int k, int mode, bool renorm, int* ids, float* weights, cudaStream_t s) {
+                      int k, int mode, bool renorm, int* ids, float* weights, float* shared_gate,
+                      cudaStream_t s) {
   if (E > 32 * kMaxExpertsPerLane) throw std::invalid_argument("moe_route: at most 512 experts");
   if (k < 1 || k > 32 || k > E) throw std::invalid_argument("moe_route: 1 <= k <= min(32, E)");
   if (T == 0) return;
   const int warps_per_block = 4;
   launch_pdl(moe_route_kernel, dim3((T + warps_per_block - 1) / warps_per_block),
              dim3(32 * warps_per_block), 0, s, logits, ld, bias, T, E, k, mode, renorm ? 1 : 0, ids,
-             weights);
+             weights, shared_gate);
 }
 
 void moe_align_launch(const int* ids, int n_assign, int e_start, int e_local, int* offsets,
@@ -281,10 +291,12 @@ void moe_act_launch(const __nv_bfloat16* gu, const __nv_bfloat16* bias, const in
 
 void moe_combine_launch(const __nv_bfloat16* y, const int* inv_pos, const float* weights,
                         const int* ids, const __nv_bfloat16* bias, int e_start, int T, int k,
-                        int H, __nv_bfloat16* out, long long ldo, cudaStream_t s) {
+                        int H, const __nv_bfloat16* shared, long long ld_shared,
+                        const float* shared_gate, __nv_bfloat16* out, long long ldo,
+                        cudaStream_t s) {
   if (T == 0) return;
   launch_pdl(moe_combine_kernel, dim3(T), dim3(256), 0, s, y, inv_pos, weights, ids, bias, e_start,
-             k, H, out, ldo);
+             k, H, shared, ld_shared, shared_gate, out, ldo);
 }
 
 }  // namespace b200

@@ -18,8 +18,11 @@ enum MoeAct : int {
                        // (up + 1) * gate * sigmoid(alpha * gate)
 };
 
+// logits [T, E (+1)]: when shared_gate is given, column E is the shared expert's gate logit
+// and shared_gate[t] = sigmoid(logits[t, E]).
 void moe_route_launch(const __nv_bfloat16* logits, long long ld, const float* bias, int T, int E,
-                      int k, int mode, bool renorm, int* ids, float* weights, cudaStream_t s);
+                      int k, int mode, bool renorm, int* ids, float* weights, float* shared_gate,
+                      cudaStream_t s);
 
 // Groups the T*k assignments by local expert [e_start, e_start + e_local).
 void moe_align_launch(const int* ids, int n_assign, int e_start, int e_local, int* offsets,
@@ -35,6 +38,8 @@ void moe_act_launch(const __nv_bfloat16* gu, const __nv_bfloat16* bias, const in
 
 void moe_combine_launch(const __nv_bfloat16* y, const int* inv_pos, const float* weights,
                         const int* ids, const __nv_bfloat16* bias, int e_start, int T, int k,
-                        int H, __nv_bfloat16* out, long long ldo, cudaStream_t s);
+                        int H, const __nv_bfloat16* shared, long long ld_shared,
+                        const float* shared_gate, __nv_bfloat16* out, long long ldo,
+                        cudaStream_t s);
 
 }  // namespace b200

@@ -1,0 +1,48 @@
+"""Model families on the GPU (bf16, sm_100a kernels) against their fp32 CPU runs of the same
+checkpoint: greedy tokens of a short generation must mostly agree."""
+import tempfile
+
+import pytest
+import torch
+
+from tests._tiny import random_prompts
+from vllm_neuron_b200.engine.sampling_params import SamplingParams
+from vllm_neuron_b200.entrypoints import LLM
+from vllm_neuron_b200.ops._ext import ext
+
+pytestmark = pytest.mark.gpu
+
+
+def _gpt_oss_ckpt():
+    from transformers import GptOssConfig, GptOssForCausalLM
+
+    torch.manual_seed(0)
+    cfg = GptOssConfig(hidden_size=256, num_hidden_layers=2, num_attention_heads=8, num_key_value_heads=2,
+                       head_dim=64, intermediate_size=256, num_local_experts=8, num_experts_per_tok=2,
+                       vocab_size=1024, sliding_window=16, max_position_embeddings=1024,
+                       layer_types=["sliding_attention", "full_attention"], initializer_range=0.05)
+    hf = GptOssForCausalLM(cfg).to(torch.bfloat16).eval()
+    d = tempfile.mkdtemp(prefix="gptoss_gpu_")
+    hf.save_pretrained(d, safe_serialization=True)
+    return d
+
+
+def _agree(d, **kw):
+    prompts = random_prompts(n=4, length=40, vocab=1024)
+    sp = SamplingParams(temperature=0, max_tokens=8, ignore_eos=True)
+    cpu = LLM(d, device="cpu", dtype="float32", max_num_seqs=4, max_model_len=256, num_gpu_blocks=64,
+              max_num_batched_tokens=256, **kw).generate(prompts, sp)
+    ext().reset_status()
+    gpu = LLM(d, device="cuda:0", max_num_seqs=4, max_model_len=256, num_gpu_blocks=64,
+              max_num_batched_tokens=256, **kw).generate(prompts, sp)
+    torch.cuda.synchronize()
+    assert ext().read_status() == 0
+    a = [o.outputs[0].token_ids for o in cpu]
+    b = [o.outputs[0].token_ids for o in gpu]
+    assert all(x[0] == y[0] for x, y in zip(a, b)), (a, b)
+    same = sum(p == q for x, y in zip(a, b) for p, q in zip(x, y))
+    assert same >= 0.7 * sum(len(x) for x in a), (a, b)
+
+
+def test_gpt_oss_gpu_matches_cpu(cuda_device):
+    _agree(_gpt_oss_ckpt())

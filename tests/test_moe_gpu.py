@@ -69,3 +69,22 @@ def test_moe_block(cuda_device, T, kind):
     ids2, w2 = M.route_ref(ws.logits[:T], k, mode, True, rb)
     ref2 = M.experts_ref(x2, ids2, w2, w_gu, w_dn, b_gu, b_dn, act, e_start=e_start)
     assert _rel_err(out2, ref2) < 2e-2
+
+
+@pytest.mark.parametrize("T", [3, 200])
+def test_moe_block_shared_expert(cuda_device, T):
+    E, k, H, I = 64, 8, 512, 256
+    g = torch.Generator(device=cuda_device).manual_seed(2)
+    x = torch.randn(T, H, device=cuda_device, generator=g).to(torch.bfloat16)
+    rw = (torch.randn(E + 1, H, device=cuda_device, generator=g) * 0.05).to(torch.bfloat16)
+    w_gu = (torch.randn(E, 2 * I, H, device=cuda_device, generator=g) * H ** -0.5).to(torch.bfloat16)
+    w_dn = (torch.randn(E, H, I, device=cuda_device, generator=g) * I ** -0.5).to(torch.bfloat16)
+    s_gu = (torch.randn(2 * I, H, device=cuda_device, generator=g) * H ** -0.5).to(torch.bfloat16)
+    s_dn = (torch.randn(H, I, device=cuda_device, generator=g) * I ** -0.5).to(torch.bfloat16)
+    ws = M.MoEWorkspace.create(256, k, E, E, H, I, cuda_device, shared_inter=I)
+    out = M.moe_block(x, rw, w_gu, w_dn, k, M.ROUTE_SOFTMAX_TOPK, True, ws=ws, num_experts=E,
+                      shared_gu=s_gu, shared_down=s_dn)
+    logits = ws.logits[:T, :E + 1]
+    ids, w = M.route_ref(logits[:, :E], k, M.ROUTE_SOFTMAX_TOPK, True)
+    ref = M.experts_ref(x, ids, w, w_gu, w_dn) + torch.sigmoid(logits[:, E:].float()) * M.shared_expert_ref(x, s_gu, s_dn)
+    assert _rel_err(out, ref) < 2e-2

@@ -1,0 +1,72 @@
+"""Qwen families on CPU (fp32) against HF transformers: Qwen3 (QK-norm dense), Qwen3-MoE
+(softmax top-k, renormalised) and Qwen2-MoE (shared expert with sigmoid gate)."""
+import tempfile
+
+import pytest
+import torch
+
+from tests._tiny import random_prompts
+from vllm_neuron_b200.engine.sampling_params import SamplingParams
+from vllm_neuron_b200.entrypoints import LLM
+
+
+def _hf_greedy(hf, prompt, n):
+    ids = torch.tensor([prompt])
+    out = []
+    with torch.no_grad():
+        for _ in range(n):
+            nxt = int(hf(ids).logits[0, -1].argmax())
+            out.append(nxt)
+            ids = torch.cat([ids, torch.tensor([[nxt]])], 1)
+    return out
+
+
+def _save(hf):
+    d = tempfile.mkdtemp(prefix="tiny_qwen_")
+    hf.save_pretrained(d, safe_serialization=True)
+    return d
+
+
+def _check(d, hf, vocab):
+    prompts = random_prompts(n=3, length=24, vocab=vocab)
+    llm = LLM(d, device="cpu", dtype="float32", max_num_seqs=4, max_model_len=128, num_gpu_blocks=64,
+              max_num_batched_tokens=64)
+    outs = llm.generate(prompts, SamplingParams(temperature=0, max_tokens=8, ignore_eos=True))
+    for p, o in zip(prompts, outs):
+        assert o.outputs[0].token_ids == _hf_greedy(hf, p, 8)
+
+
+def test_qwen3_dense():
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+
+    torch.manual_seed(0)
+    cfg = Qwen3Config(hidden_size=64, num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
+                      head_dim=16, intermediate_size=128, vocab_size=512, max_position_embeddings=256,
+                      initializer_range=0.05, tie_word_embeddings=False)
+    hf = Qwen3ForCausalLM(cfg).float().eval()
+    _check(_save(hf), hf, 512)
+
+
+@pytest.mark.parametrize("renorm", [True, False])
+def test_qwen3_moe(renorm):
+    from transformers import Qwen3MoeConfig, Qwen3MoeForCausalLM
+
+    torch.manual_seed(1)
+    cfg = Qwen3MoeConfig(hidden_size=64, num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
+                         head_dim=16, intermediate_size=128, moe_intermediate_size=32, num_experts=8,
+                         num_experts_per_tok=2, norm_topk_prob=renorm, vocab_size=512,
+                         max_position_embeddings=256, initializer_range=0.05)
+    hf = Qwen3MoeForCausalLM(cfg).float().eval()
+    _check(_save(hf), hf, 512)
+
+
+def test_qwen2_moe_shared_expert():
+    from transformers import Qwen2MoeConfig, Qwen2MoeForCausalLM
+
+    torch.manual_seed(2)
+    cfg = Qwen2MoeConfig(hidden_size=64, num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
+                         intermediate_size=128, moe_intermediate_size=32, shared_expert_intermediate_size=48,
+                         num_experts=8, num_experts_per_tok=2, norm_topk_prob=False, vocab_size=512,
+                         max_position_embeddings=256, initializer_range=0.05, qkv_bias=True)
+    hf = Qwen2MoeForCausalLM(cfg).float().eval()
+    _check(_save(hf), hf, 512)

@@ -1,0 +1,118 @@
+"""Qwen mixture-of-experts decoders on the dense attention path of :mod:`.llama`:
+
+* ``Qwen3MoeForCausalLM``: softmax routing over all experts, top-k, optional renormalisation
+  (``norm_topk_prob``), SiLU experts, QK-norm attention;
+* ``Qwen2MoeForCausalLM``: the same plus a shared expert whose output is scaled by
+  ``sigmoid(x . shared_expert_gate)``.
+
+Experts are sharded by index over the tensor-parallel ranks (expert parallelism over the TP
+group); the shared expert is sharded by its intermediate dimension like a dense MLP, so the
+partial outputs of all ranks sum to the full block output in the all-reduce.  The shared
+expert's gate is appended to the router as row ``E`` (one GEMM for both).
+
+Reference: the MoE block semantics of vllm_neuron/functional/moe/moe_block_tkg.py:306
+(router + experts + shared expert) and router.py:72 (softmax -> top-k -> renormalise).
+"""
+from __future__ import annotations
+
+import torch
+
+from .. import ops
+from ..ops import moe as M
+from .llama import LlamaForCausalLM
+
+
+class MoEMixin:
+    """Routed-experts MLP for decoder models built on :class:`LlamaForCausalLM`."""
+
+    route_mode = M.ROUTE_SOFTMAX_TOPK
+    expert_act = M.ACT_SILU
+
+    def _init_moe(self, cfg, tp):
+        W = tp.world if tp is not None else 1
+        self.E = cfg.num_experts
+        self.topk = cfg.num_experts_per_tok
+        assert self.E % W == 0, f"{self.E} experts not divisible by TP={W}"
+        self.e_local = self.E // W
+        self.I_moe = cfg.moe_intermediate_size or cfg.intermediate_size
+        self.I_sh = (cfg.shared_expert_intermediate_size or 0) // W
+        self.renorm = bool(cfg.norm_topk_prob)
+
+    def _post_init_moe(self):
+        self.e_start = self.tp.rank * self.e_local
+        self.moe_ws = None
+        if self.device.type == "cuda":
+            self.moe_ws = M.MoEWorkspace.create(self.max_tokens, self.topk, self.E, self.e_local, self.H,
+                                                self.I_moe, self.device, shared_inter=self.I_sh)
+
+    def _moe_params(self, m, p):
+        m.router = p(self.E + (1 if self.I_sh else 0), self.H)
+        m.w_gu = p(self.e_local, 2 * self.I_moe, self.H)
+        m.w_down = p(self.e_local, self.H, self.I_moe)
+        if self.I_sh:
+            m.sh_gu = p(2 * self.I_sh, self.H)
+            m.sh_down = p(self.H, self.I_sh)
+        else:
+            m.sh_gu = m.sh_down = None
+
+    def _moe_mlp(self, ly, x, res, nxt_norm, T):
+        h = self.ws_h[:T]
+        M.moe_block(x, ly.router, ly.w_gu, ly.w_down, self.topk, self.route_mode, self.renorm,
+                    act=self.expert_act, e_start=self.e_start, ws=self.moe_ws, out=h,
+                    num_experts=self.E, shared_gu=ly.sh_gu, shared_down=ly.sh_down)
+        self.tp.all_reduce_(h)
+        ops.add_rmsnorm(h, res, nxt_norm, self.eps, out=x)
+
+
+class Qwen3MoeForCausalLM(MoEMixin, LlamaForCausalLM):
+    def __init__(self, cfg, *args, **kw):
+        self._init_moe(cfg, kw.get("tp"))
+        super().__init__(cfg, *args, **kw)
+        self._post_init_moe()
+
+    def _make_mlp(self, m, p, layer: int):
+        self._moe_params(m, p)
+
+    def _mlp(self, i, ly, x, res, nxt_norm, T, small, fused):
+        self._moe_mlp(ly, x, res, nxt_norm, T)
+
+    def load_hf_state_dict(self, get_tensor, names: set[str]):
+        from ..utils.weight_loader import load_dense_decoder
+
+        load_dense_decoder(self, get_tensor, names, mlp_loader=load_moe_mlp)
+
+
+class Qwen2MoeForCausalLM(Qwen3MoeForCausalLM):
+    pass
+
+
+@torch.no_grad()
+def load_moe_mlp(model, ly, get_tensor, names: set[str], p: str):
+    """Router (+ shared expert gate), experts ``[e_start, e_start + e_local)`` and the TP shard
+    of the shared expert, from fused (``experts.gate_up_proj [E, 2I, H]``) or per-expert
+    (``experts.{e}.gate_proj.weight``) checkpoints."""
+    from ..utils.weight_loader import _copy, shard_cols, shard_rows
+
+    W, r = model.tp.world, model.tp.rank
+    e0, el = model.e_start, model.e_local
+    router = get_tensor(p + "mlp.gate.weight")
+    if model.I_sh:
+        router = torch.cat([router, get_tensor(p + "mlp.shared_expert_gate.weight").reshape(1, -1)], 0)
+    _copy(ly.router, router, p + "router")
+    fused = p + "mlp.experts.gate_up_proj"
+    if fused in names:
+        gu = get_tensor(fused)[e0:e0 + el]
+        dn = get_tensor(p + "mlp.experts.down_proj")[e0:e0 + el]
+    else:
+        gu = torch.stack([torch.cat([get_tensor(f"{p}mlp.experts.{e}.gate_proj.weight"),
+                                     get_tensor(f"{p}mlp.experts.{e}.up_proj.weight")], 0)
+                          for e in range(e0, e0 + el)])
+        dn = torch.stack([get_tensor(f"{p}mlp.experts.{e}.down_proj.weight") for e in range(e0, e0 + el)])
+    _copy(ly.w_gu, gu, p + "w_gu")
+    _copy(ly.w_down, dn, p + "w_down")
+    if model.I_sh:
+        g = shard_rows(get_tensor(p + "mlp.shared_expert.gate_proj.weight"), W, r)
+        u = shard_rows(get_tensor(p + "mlp.shared_expert.up_proj.weight"), W, r)
+        _copy(ly.sh_gu, torch.cat([g, u], 0), p + "shared_expert.gate_up")
+        _copy(ly.sh_down, shard_cols(get_tensor(p + "mlp.shared_expert.down_proj.weight"), W, r),
+              p + "shared_expert.down")

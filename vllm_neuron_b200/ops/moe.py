@@ -51,6 +51,10 @@ class MoEWorkspace:
     gtiles: torch.Tensor
     gcount: torch.Tensor
     logits: torch.Tensor
+    shared_gate: torch.Tensor
+    shared: torch.Tensor
+    shared_gu: torch.Tensor
+    shared_act: torch.Tensor
     xp: torch.Tensor
     gu: torch.Tensor
     act: torch.Tensor
@@ -58,7 +62,7 @@ class MoEWorkspace:
 
     @classmethod
     def create(cls, max_tokens: int, k: int, num_experts: int, e_local: int, hidden: int,
-               inter: int, device, dtype=torch.bfloat16) -> "MoEWorkspace":
+               inter: int, device, dtype=torch.bfloat16, shared_inter: int = 0) -> "MoEWorkspace":
         R = max_tokens * k
         gmax = R // 128 + e_local + 1
         i32 = dict(dtype=torch.int32, device=device)
@@ -71,7 +75,11 @@ class MoEWorkspace:
             inv_pos=torch.zeros(R, **i32),
             gtiles=torch.zeros(gmax, 4, **i32),
             gcount=torch.zeros(1, **i32),
-            logits=torch.zeros(max_tokens, num_experts, dtype=dtype, device=device),
+            logits=torch.zeros(max_tokens, num_experts + 1, dtype=dtype, device=device),
+            shared_gate=torch.zeros(max_tokens, dtype=torch.float32, device=device),
+            shared=torch.zeros(max_tokens, hidden, dtype=dtype, device=device),
+            shared_gu=torch.zeros(max_tokens if shared_inter else 0, 2 * shared_inter, dtype=dtype, device=device),
+            shared_act=torch.zeros(max_tokens if shared_inter else 0, shared_inter, dtype=dtype, device=device),
             xp=torch.zeros(R, hidden, dtype=dtype, device=device),
             gu=torch.zeros(R, 2 * inter, dtype=dtype, device=device),
             act=torch.zeros(R, inter, dtype=dtype, device=device),
@@ -132,10 +140,16 @@ def experts_ref(x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, w_gu: torch
 # ------------------------------------------------------------------------------ kernels
 def route(logits: torch.Tensor, k: int, mode: int, renorm: bool = True,
           bias: torch.Tensor | None = None, ids: torch.Tensor | None = None,
-          weights: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+          weights: torch.Tensor | None = None, num_experts: int | None = None,
+          shared_gate: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Top-k routing of ``logits [T, E]``.  With ``num_experts = E`` and ``logits [T, E + 1]``
+    the last column is a shared expert's gate logit and ``shared_gate[t]`` receives its sigmoid."""
     T = logits.shape[0]
+    E = num_experts or logits.shape[1]
     if not logits.is_cuda:
-        i, v = route_ref(logits, k, mode, renorm, bias)
+        i, v = route_ref(logits[:, :E], k, mode, renorm, bias)
+        if shared_gate is not None:
+            shared_gate[:T].copy_(torch.sigmoid(logits[:, E].float()))
         if ids is not None:
             ids[:T].copy_(i)
             weights[:T].copy_(v)
@@ -145,42 +159,66 @@ def route(logits: torch.Tensor, k: int, mode: int, renorm: bool = True,
         ids = torch.empty(T, k, dtype=torch.int32, device=logits.device)
         weights = torch.empty(T, k, dtype=torch.float32, device=logits.device)
     ids, weights = ids[:T], weights[:T]
-    ext().moe_route(logits, bias, k, mode, renorm, ids, weights)
+    ext().moe_route(logits, bias, E, k, mode, renorm, ids, weights,
+                    shared_gate[:T] if shared_gate is not None else None)
     return ids, weights
+
+
+def shared_expert_ref(x: torch.Tensor, w_gu: torch.Tensor, w_down: torch.Tensor) -> torch.Tensor:
+    I = w_gu.shape[0] // 2
+    h = x.float() @ w_gu.float().t()
+    return (torch.nn.functional.silu(h[:, :I]) * h[:, I:]) @ w_down.float().t()
 
 
 def moe_block(x: torch.Tensor, router_w: torch.Tensor, w_gu: torch.Tensor, w_down: torch.Tensor,
               k: int, mode: int, renorm: bool = True, router_b: torch.Tensor | None = None,
               b_gu: torch.Tensor | None = None, b_down: torch.Tensor | None = None,
               act: int = ACT_SILU, alpha: float = 1.702, limit: float = 7.0, e_start: int = 0,
-              ws: MoEWorkspace | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+              ws: MoEWorkspace | None = None, out: torch.Tensor | None = None,
+              num_experts: int | None = None, shared_gu: torch.Tensor | None = None,
+              shared_down: torch.Tensor | None = None) -> torch.Tensor:
     """Routed experts for ``x [T, H]`` (see the module docstring); returns ``out [T, H]`` bf16.
 
     ``w_gu [e_local, 2I, H]`` holds each expert's gate rows followed by its up rows,
     ``w_down [e_local, H, I]``; biases are bf16 ``[e_local, 2I]`` / ``[e_local, H]`` and the
-    router bias fp32 ``[E]``.
+    router bias fp32 ``[E]``.  With a shared expert (``shared_gu [2Is, H]`` gate rows then up
+    rows, ``shared_down [H, Is]``) ``router_w`` has ``E + 1`` rows, the last being the shared
+    expert's gate, and ``out += sigmoid(x . gate) * shared_expert(x)``.
     """
     T, H = x.shape
     e_local, I2, _ = w_gu.shape
     I = I2 // 2
+    E = num_experts or router_w.shape[0]
+    has_shared = shared_gu is not None
     if out is None:
         out = torch.empty(T, H, dtype=torch.bfloat16, device=x.device)
     if not x.is_cuda:
         logits = (x.float() @ router_w.float().t()).to(x.dtype)
-        ids, w = route_ref(logits, k, mode, renorm, router_b)
-        out.copy_(experts_ref(x, ids, w, w_gu, w_down, b_gu, b_down, act, alpha, limit, e_start).to(out.dtype))
+        ids, w = route_ref(logits[:, :E], k, mode, renorm, router_b)
+        r = experts_ref(x, ids, w, w_gu, w_down, b_gu, b_down, act, alpha, limit, e_start)
+        if has_shared:
+            r = r + torch.sigmoid(logits[:, E:E + 1].float()) * shared_expert_ref(x, shared_gu, shared_down)
+        out.copy_(r.to(out.dtype))
         return out
     if T == 0:
         return out
-    E = router_w.shape[0]
     if ws is None:
-        ws = MoEWorkspace.create(T, k, E, e_local, H, I, x.device)
-    logits = ws.logits[:T]
+        ws = MoEWorkspace.create(T, k, E, e_local, H, I, x.device,
+                                 shared_inter=shared_gu.shape[0] // 2 if has_shared else 0)
+    logits = ws.logits[:T, :router_w.shape[0]]
     if T <= L.SKINNY_MAX:
         L.gemm_skinny_bf16(x, router_w, out=logits)
     else:
         L.gemm_out(x, router_w, out=logits)
-    ids, w = route(logits, k, mode, renorm, router_b, ws.ids, ws.weights)
+    ids, w = route(logits, k, mode, renorm, router_b, ws.ids, ws.weights, E,
+                   ws.shared_gate if has_shared else None)
+    shared = None
+    if has_shared:
+        from .activation import silu_mul
+
+        gu_sh = L.gemm_out(x, shared_gu, out=ws.shared_gu[:T])
+        a_sh = silu_mul(gu_sh, out=ws.shared_act[:T])
+        shared = L.gemm_out(a_sh, shared_down, out=ws.shared[:T])
     R = T * k
     ext().moe_align(ids, e_start, e_local, ws.offsets, ws.sorted_src, ws.row_expert,
                     ws.inv_pos[:R], ws.gtiles, ws.gcount)
@@ -188,9 +226,10 @@ def moe_block(x: torch.Tensor, router_w: torch.Tensor, w_gu: torch.Tensor, w_dow
     ext().moe_gather(x, ws.sorted_src, k, ws.offsets, xp)
     gu = ws.gu[:R]
     ext().gemm_grouped(xp, w_gu, gu, ws.gtiles, ws.gcount, EPI_BF16, 256)
-    a = ws.act[:R]
+    a = ws.act[:R, :I]
     ext().moe_act(gu, b_gu, ws.row_expert, ws.offsets, act, alpha, limit, a)
     y = ws.y[:R]
     ext().gemm_grouped(a, w_down, y, ws.gtiles, ws.gcount, EPI_BF16, 256 if H % 256 == 0 else 128)
-    ext().moe_combine(y, ws.inv_pos[:R], w, ids, b_down, e_start, out)
+    ext().moe_combine(y, ws.inv_pos[:R], w, ids, b_down, e_start, shared,
+                      ws.shared_gate[:T] if has_shared else None, out)
     return out

@@ -55,7 +55,10 @@ def _copy(dst: torch.nn.Parameter, src: torch.Tensor, name: str):
 
 
 @torch.no_grad()
-def load_dense_decoder(model, get_tensor: Callable[[str], torch.Tensor], names: set[str]):
+def load_dense_decoder(model, get_tensor: Callable[[str], torch.Tensor], names: set[str],
+                       mlp_loader: Callable | None = None):
+    """Llama/Qwen-style decoder; ``mlp_loader(model, layer, get_tensor, names, prefix)``
+    replaces the dense MLP loading (MoE models)."""
     cfg = model.cfg
     W, r = model.tp.world, model.tp.rank
     pre = "model." if any(n.startswith("model.") for n in names) else ""
@@ -79,6 +82,9 @@ def load_dense_decoder(model, get_tensor: Callable[[str], torch.Tensor], names: 
         if ly.q_norm is not None:
             _copy(ly.q_norm, get_tensor(p + "self_attn.q_norm.weight"), p + "q_norm")
             _copy(ly.k_norm, get_tensor(p + "self_attn.k_norm.weight"), p + "k_norm")
+        if mlp_loader is not None:
+            mlp_loader(model, ly, get_tensor, names, p)
+            continue
         g = shard_rows(get_tensor(p + "mlp.gate_proj.weight"), W, r)
         u = shard_rows(get_tensor(p + "mlp.up_proj.weight"), W, r)
         gu = L.interleave_gate_up(g, u) if model.silu_blk else torch.cat([g, u], 0)
