@@ -14,6 +14,7 @@
 #include "gemm/gemm.h"
 #include "misc/misc.h"
 #include "moe/moe.h"
+#include "deltanet/deltanet.h"
 
 namespace {
 
@@ -482,6 +483,89 @@ void moe_combine(const at::Tensor& y, const at::Tensor& inv_pos, const at::Tenso
   check_launch("moe_combine", T > 0 ? 1 : 0);
 }
 
+// ------------------------------------------------------------------------- DeltaNet
+static b200::LinearAttnBatch linear_batch(const at::Tensor& q_start, const at::Tensor& seq_lens,
+                                          const at::Tensor& slots) {
+  TORCH_CHECK(q_start.scalar_type() == at::kInt && seq_lens.scalar_type() == at::kInt &&
+                  slots.scalar_type() == at::kInt,
+              "batch metadata must be int32");
+  b200::LinearAttnBatch b{};
+  b.q_start = q_start.data_ptr<int>();
+  b.seq_lens = seq_lens.data_ptr<int>();
+  b.slots = slots.data_ptr<int>();
+  b.B = (int)seq_lens.size(0);
+  return b;
+}
+
+void causal_conv1d(const at::Tensor& x, const at::Tensor& w, const at::Tensor& q_start,
+                   const at::Tensor& seq_lens, const at::Tensor& slots, at::Tensor& state,
+                   at::Tensor& y) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  CHECK_BF16(w);
+  CHECK_BF16(state);
+  CHECK_BF16(y);
+  TORCH_CHECK(x.stride(1) == 1 && y.stride(1) == 1 && w.is_contiguous(), "causal_conv1d: layouts");
+  TORCH_CHECK(state.dim() == 3 && state.size(1) == x.size(1) && state.size(2) == w.size(1) - 1 &&
+                  state.stride(2) == 1 && state.stride(1) == state.size(2),
+              "causal_conv1d: state must be [slots, C, K - 1]");
+  const c10::cuda::CUDAGuard guard(x.device());
+  b200::causal_conv1d_launch(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0),
+                             (int)x.size(1), reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
+                             (int)w.size(1), linear_batch(q_start, seq_lens, slots),
+                             reinterpret_cast<__nv_bfloat16*>(state.data_ptr()), state.stride(0),
+                             reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), y.stride(0), cur_stream());
+  check_launch("causal_conv1d", seq_lens.size(0) > 0 ? 1 : 0);
+}
+
+void gated_delta_rule(const at::Tensor& qkv, const at::Tensor& z, const at::Tensor& a,
+                      const at::Tensor& b, const at::Tensor& A_log, const at::Tensor& dt_bias,
+                      const at::Tensor& norm_w, double eps, const at::Tensor& q_start,
+                      const at::Tensor& seq_lens, const at::Tensor& slots, at::Tensor& state,
+                      at::Tensor& out, int64_t Hk, int64_t Hv) {
+  CHECK_CUDA(qkv);
+  CHECK_BF16(qkv);
+  CHECK_BF16(z);
+  CHECK_BF16(out);
+  TORCH_CHECK(state.scalar_type() == at::kFloat && state.dim() == 4 && state.is_contiguous(),
+              "gated_delta_rule: state must be fp32 [slots, Hv, dk, dv]");
+  TORCH_CHECK(z.stride(0) == a.stride(0) && z.stride(0) == b.stride(0), "z, a, b must share a row stride");
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  b200::GatedDeltaParams p{};
+  p.qkv = reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr());
+  p.ld_qkv = qkv.stride(0);
+  p.z = reinterpret_cast<const __nv_bfloat16*>(z.data_ptr());
+  p.a = reinterpret_cast<const __nv_bfloat16*>(a.data_ptr());
+  p.b = reinterpret_cast<const __nv_bfloat16*>(b.data_ptr());
+  p.ld_zab = z.stride(0);
+  p.A_log = A_log.data_ptr<float>();
+  p.dt_bias = dt_bias.data_ptr<float>();
+  p.norm_w = reinterpret_cast<const __nv_bfloat16*>(norm_w.data_ptr());
+  p.eps = (float)eps;
+  p.state = state.data_ptr<float>();
+  p.state_slot_stride = state.stride(0);
+  p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  p.ld_out = out.stride(0);
+  p.Hk = (int)Hk;
+  p.Hv = (int)Hv;
+  p.dk = (int)state.size(2);
+  p.dv = (int)state.size(3);
+  b200::gated_delta_rule_launch(p, linear_batch(q_start, seq_lens, slots), cur_stream());
+  check_launch("gated_delta_rule", seq_lens.size(0) > 0 ? 1 : 0);
+}
+
+void sigmoid_gate_mul(at::Tensor& x, const at::Tensor& gate) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  CHECK_BF16(gate);
+  TORCH_CHECK(x.stride(1) == 1 && gate.stride(1) == 1 && x.sizes() == gate.sizes(), "sigmoid_gate_mul: layouts");
+  const c10::cuda::CUDAGuard guard(x.device());
+  b200::sigmoid_gate_mul_launch(reinterpret_cast<__nv_bfloat16*>(x.data_ptr()), x.stride(0),
+                                reinterpret_cast<const __nv_bfloat16*>(gate.data_ptr()), gate.stride(0),
+                                (int)x.size(0), (int)x.size(1), cur_stream());
+  check_launch("sigmoid_gate_mul", x.size(0) > 0 ? 1 : 0);
+}
+
 int64_t num_sms() { return b200::num_sms_cached(); }
 int64_t launch_count() { return g_launches.load(); }
 
@@ -513,4 +597,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_gather", &moe_gather);
   m.def("moe_act", &moe_act);
   m.def("moe_combine", &moe_combine);
+  m.def("causal_conv1d", &causal_conv1d);
+  m.def("gated_delta_rule", &gated_delta_rule);
+  m.def("sigmoid_gate_mul", &sigmoid_gate_mul);
 }

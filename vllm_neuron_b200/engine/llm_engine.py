@@ -107,7 +107,10 @@ class LLMEngine:
             nb = int(t.item())
         self.runner.allocate_kv_cache(nb)
         self.metrics = Metrics()
-        self.block_manager = BlockManager(nb, args.block_size, args.enable_prefix_caching)
+        # Models with per-request recurrent state (linear attention) cannot reuse cached KV
+        # prefixes: the state after the prefix is not stored with the blocks.
+        apc = args.enable_prefix_caching and getattr(self.model, "supports_prefix_caching", True)
+        self.block_manager = BlockManager(nb, args.block_size, apc)
         self.scheduler = Scheduler(self.block_manager, args.max_num_seqs, max_tok, self.max_model_len,
                                    enable_chunked_prefill=args.enable_chunked_prefill,
                                    num_batched_tokens_buckets=self.b200_config.num_batched_tokens_buckets,

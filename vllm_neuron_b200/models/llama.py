@@ -52,6 +52,7 @@ class ForwardBatch:
     num_splits: int
     num_tokens: int
     last_tok: torch.Tensor | None = None  # device-resident tokens for ids < 0
+    seq_slots: torch.Tensor | None = None  # [B] int32 per-request state-cache slots
 
 
 def _shard(n: int, world: int, rank: int) -> tuple[int, int]:
@@ -97,18 +98,8 @@ class LlamaForCausalLM(torch.nn.Module):
             m = torch.nn.Module()
             m.input_norm = p(self.H)
             m.post_norm = p(self.H)
-            m.qkv = p(qkv_out, self.H)
-            m.qkv_bias = p(qkv_out) if cfg.attention_bias else None
-            m.o = p(self.H, self.Hq * self.D)
-            m.o_bias = None
-            m.window = cfg.sliding_window if cfg.layer_is_sliding(len(self.layers)) else 0
-            m.sinks = None
+            self._make_attn(m, p, len(self.layers))
             self._make_mlp(m, p, len(self.layers))
-            if cfg.qk_norm:
-                m.q_norm = p(self.D)
-                m.k_norm = p(self.D)
-            else:
-                m.q_norm = m.k_norm = None
             self.layers.append(m)
         self.final_norm = p(self.H)
         self.lm_head = self.embed if cfg.tie_word_embeddings else p(self.V_local, self.H)
@@ -119,6 +110,21 @@ class LlamaForCausalLM(torch.nn.Module):
         self.tp_fused = None  # TPFusedComm: fused all-reduce + residual + RMSNorm (decode)
 
     # ---------------------------------------------------------------- init / weights
+    def _make_attn(self, m, p, layer: int):
+        """Attention parameters of one layer."""
+        cfg = self.cfg
+        m.qkv = p(self.qkv_out, self.H)
+        m.qkv_bias = p(self.qkv_out) if cfg.attention_bias else None
+        m.o = p(self.H, self.Hq * self.D)
+        m.o_bias = None
+        m.window = cfg.sliding_window if cfg.layer_is_sliding(layer) else 0
+        m.sinks = None
+        if cfg.qk_norm:
+            m.q_norm = p(self.D)
+            m.k_norm = p(self.D)
+        else:
+            m.q_norm = m.k_norm = None
+
     def _make_mlp(self, m, p, layer: int):
         """Dense SwiGLU MLP parameters of one layer (MoE models override this)."""
         m.gate_up = p(2 * self.I, self.H)
@@ -167,15 +173,19 @@ class LlamaForCausalLM(torch.nn.Module):
 
             self.tp_fused = TPFusedComm(self.tp, self.H, self.max_decode_tokens, self.device, cpu_group)
 
+    @property
+    def num_kv_layers(self) -> int:
+        return self.cfg.num_layers
+
     def bind_kv_cache(self, kv_caches: list[tuple[torch.Tensor, torch.Tensor]]):
-        assert len(kv_caches) == self.cfg.num_layers
+        assert len(kv_caches) == self.num_kv_layers
         self.kv_caches = kv_caches
 
     def kv_cache_shape(self, num_blocks: int) -> tuple[int, ...]:
         return (num_blocks, self.Hkv, self.block_size, self.D)
 
     def kv_bytes_per_block(self) -> int:
-        return 2 * self.cfg.num_layers * self.Hkv * self.block_size * self.D * 2
+        return 2 * self.num_kv_layers * self.Hkv * self.block_size * self.D * 2
 
     # ---------------------------------------------------------------- forward
     @torch.no_grad()

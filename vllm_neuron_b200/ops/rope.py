@@ -118,7 +118,7 @@ def rope_kv_write_ref(qkv, positions, cos_sin, Hq, Hkv, D, q_out, k_cache, v_cac
     from .norm import rmsnorm_ref
 
     T = qkv.shape[0]
-    x = qkv.float().view(T, Hq + 2 * Hkv, D)
+    x = qkv[:, :(Hq + 2 * Hkv) * D].float().reshape(T, Hq + 2 * Hkv, D)
     q, k, v = x[:, :Hq], x[:, Hq:Hq + Hkv], x[:, Hq + Hkv:]
     if q_norm_w is not None:
         q = rmsnorm_ref(q, q_norm_w, eps).to(torch.bfloat16).float()

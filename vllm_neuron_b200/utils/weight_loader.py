@@ -153,3 +153,58 @@ def load_gpt_oss(model, get_tensor: Callable[[str], torch.Tensor], names: set[st
         _copy(ly.b_down, get_tensor(dn_name + "_bias")[e0:e0 + el], p + "b_down")
     _copy(model.final_norm, get_tensor(pre + "norm.weight"), "norm")
     _copy(model.lm_head, shard_rows(get_tensor("lm_head.weight"), W, r, model.V_local), "lm_head")
+
+
+@torch.no_grad()
+def load_qwen3_5(model, get_tensor: Callable[[str], torch.Tensor], names: set[str]):
+    """Hybrid Qwen3.5/3.6 text decoder.  RMSNorm weights are stored as offsets from 1 and are
+    converted to scales; linear-attention heads/channels and attention heads are split over
+    the TP ranks; experts by index (see :func:`..models.qwen_moe.load_moe_mlp`)."""
+    from ..models.qwen_moe import load_moe_mlp
+
+    cfg = model.cfg
+    W, r = model.tp.world, model.tp.rank
+    pre = "model.language_model." if any(n.startswith("model.language_model.") for n in names) else "model."
+    one = lambda t: t.float() + 1.0  # noqa: E731
+    _copy(model.embed, shard_rows(get_tensor(pre + "embed_tokens.weight"), W, r, model.V_local), "embed")
+    Hk, Hv, dk, dv = model.lin_Hk, model.lin_Hv, model.lin_dk, model.lin_dv
+    Kd, Vd = cfg.linear_num_key_heads * dk, cfg.linear_num_value_heads * dv
+    for i, ly in enumerate(model.layers):
+        p = f"{pre}layers.{i}."
+        _copy(ly.input_norm, one(get_tensor(p + "input_layernorm.weight")), p + "input_layernorm")
+        _copy(ly.post_norm, one(get_tensor(p + "post_attention_layernorm.weight")), p + "post_attention_layernorm")
+        if model.is_linear[i]:
+            a = p + "linear_attn."
+            qkv = get_tensor(a + "in_proj_qkv.weight")
+            q = qkv[:Kd][r * Hk * dk:(r + 1) * Hk * dk]
+            k = qkv[Kd:2 * Kd][r * Hk * dk:(r + 1) * Hk * dk]
+            v = qkv[2 * Kd:2 * Kd + Vd][r * Hv * dv:(r + 1) * Hv * dv]
+            z = get_tensor(a + "in_proj_z.weight")[r * Hv * dv:(r + 1) * Hv * dv]
+            bw = get_tensor(a + "in_proj_b.weight")[r * Hv:(r + 1) * Hv]
+            aw = get_tensor(a + "in_proj_a.weight")[r * Hv:(r + 1) * Hv]
+            _copy(ly.w_in, torch.cat([q, k, v, z, bw, aw], 0), a + "in_proj")
+            cw = get_tensor(a + "conv1d.weight").reshape(2 * Kd + Vd, -1)
+            cw = torch.cat([cw[:Kd][r * Hk * dk:(r + 1) * Hk * dk], cw[Kd:2 * Kd][r * Hk * dk:(r + 1) * Hk * dk],
+                            cw[2 * Kd:][r * Hv * dv:(r + 1) * Hv * dv]], 0)
+            _copy(ly.conv_w, cw, a + "conv1d")
+            _copy(ly.A_log, get_tensor(a + "A_log")[r * Hv:(r + 1) * Hv].float(), a + "A_log")
+            _copy(ly.dt_bias, get_tensor(a + "dt_bias")[r * Hv:(r + 1) * Hv].float(), a + "dt_bias")
+            _copy(ly.gnorm_w, get_tensor(a + "norm.weight"), a + "norm")
+            _copy(ly.out_proj, get_tensor(a + "out_proj.weight")[:, r * Hv * dv:(r + 1) * Hv * dv], a + "out_proj")
+        else:
+            a = p + "self_attn."
+            D = cfg.head_dim
+            qg = get_tensor(a + "q_proj.weight").view(cfg.num_heads, 2, D, -1)
+            qw, gw = qg[:, 0].reshape(cfg.num_heads * D, -1), qg[:, 1].reshape(cfg.num_heads * D, -1)
+            qkv = fused_qkv(qw, get_tensor(a + "k_proj.weight"), get_tensor(a + "v_proj.weight"),
+                            cfg.num_heads, cfg.num_kv_heads, D, W, r)
+            gate = gw[r * model.Hq * D:(r + 1) * model.Hq * D]
+            _copy(ly.qkvg, torch.cat([qkv, gate], 0), a + "qkvg")
+            _copy(ly.q_norm, one(get_tensor(a + "q_norm.weight")), a + "q_norm")
+            _copy(ly.k_norm, one(get_tensor(a + "k_norm.weight")), a + "k_norm")
+            _copy(ly.o, shard_cols(get_tensor(a + "o_proj.weight"), W, r), a + "o_proj")
+        load_moe_mlp(model, ly, get_tensor, names, p)
+    _copy(model.final_norm, one(get_tensor(pre + "norm.weight")), "norm")
+    if cfg.tie_word_embeddings:
+        return
+    _copy(model.lm_head, shard_rows(get_tensor("lm_head.weight"), W, r, model.V_local), "lm_head")

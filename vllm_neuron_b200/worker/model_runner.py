@@ -48,7 +48,7 @@ class Layout:
                         ("seqlen", self.B), ("lidx", self.S), ("work", 2 * self.W),
                         ("bt", self.B * self.nblk), ("temp", self.S), ("topk", self.S),
                         ("topp", self.S), ("minp", self.S), ("seed", 2 * self.S), ("offs", self.S),
-                        ("rslot", self.S)):
+                        ("rslot", self.S), ("sslot", self.B)):
             self.off[name] = (o, n)
             o += _round(n)
         self.total = o
@@ -112,9 +112,10 @@ class ModelRunner:
 
     def allocate_kv_cache(self, num_blocks: int):
         m = self.model
-        shape = (m.cfg.num_layers, 2) + m.kv_cache_shape(num_blocks)
+        n_kv = getattr(m, "num_kv_layers", m.cfg.num_layers)
+        shape = (n_kv, 2) + m.kv_cache_shape(num_blocks)
         self.kv_cache = torch.zeros(shape, dtype=m.dtype, device=self.device)
-        m.bind_kv_cache([(self.kv_cache[i, 0], self.kv_cache[i, 1]) for i in range(m.cfg.num_layers)])
+        m.bind_kv_cache([(self.kv_cache[i, 0], self.kv_cache[i, 1]) for i in range(n_kv)])
         self.num_blocks = num_blocks
 
     def profile_num_blocks(self, gpu_memory_utilization: float, reserve_bytes: int = 2 << 30) -> int:
@@ -157,6 +158,7 @@ class ModelRunner:
         seed = h[o["seed"][0]:o["seed"][0] + 2 * lay.S].view(np.int64)
         offs = h[o["offs"][0]:o["offs"][0] + lay.S]
         rslot = h[o["rslot"][0]:o["rslot"][0] + lay.S]
+        sslot = h[o["sslot"][0]:o["sslot"][0] + Bp]
         for i, sr in enumerate(sch):
             req = sr.req
             n = sr.num_tokens
@@ -183,6 +185,7 @@ class ModelRunner:
             qst[i] = t
             sl[i] = st + n
             q_lens[i] = n
+            sslot[i] = req.slot
             nb = len(req.block_ids)
             bt[i, :nb] = blocks
             bt[i, nb:] = 0
@@ -207,6 +210,7 @@ class ModelRunner:
             sl[i] = 1
             q_lens[i] = 1
             bt[i, :] = 0
+            sslot[i] = self.pad_slot
             lidx[s] = t
             temp[s] = 0.0
             topk[s] = 0
@@ -244,6 +248,7 @@ class ModelRunner:
             q_start=sec("qstart", B + 1), work=sec("work", 2 * W).view(W, 2),
             logits_indices=sec("lidx", S),
             decode=decode, num_splits=splits, num_tokens=lay.T)
+        fb.seq_slots = sec("sslot", B)
         samp = dict(temperature=sec("temp", S, torch.float32), top_k=sec("topk", S),
                     top_p=sec("topp", S, torch.float32), min_p=sec("minp", S, torch.float32),
                     seeds=sec("seed", 2 * S).view(torch.int64), offsets=sec("offs", S),
@@ -283,6 +288,7 @@ class ModelRunner:
             h[o["work"][0]:o["work"][0] + 2 * b] = torch.from_numpy(w.work.reshape(-1))
             h[o["topp"][0]:o["topp"][0] + b] = torch.tensor([1.0] * b).view(torch.int32)
             h[o["rslot"][0]:o["rslot"][0] + b] = self.pad_slot
+            h[o["sslot"][0]:o["sslot"][0] + b] = self.pad_slot
             buf.copy_(h)
             fb, samp = self._views(buf, lay, b, b, b, True, w.num_splits)
             tok = torch.zeros(b, dtype=torch.int32, device=self.device)
