@@ -42,6 +42,6 @@ void paged_attention_launch(const PagedAttnParams& p, int num_work, int head_dim
 bool paged_decode_tma_supported(const PagedAttnParams& p, int head_dim);
 void paged_decode_tma_launch(const PagedAttnParams& p, int num_work, int head_dim,
                              cudaStream_t stream);
-int paged_decode_warps_per_cta();
+int paged_decode_warps_per_cta(int head_dim);
 
 }  // namespace b200

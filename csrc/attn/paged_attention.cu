@@ -429,6 +429,8 @@ void paged_attention_launch(const PagedAttnParams& p, int num_work, int head_dim
   } else if (head_dim == 64) {
     decode ? launch_attn<64, true>(p, num_work, stream)
            : launch_attn<64, false>(p, num_work, stream);
+  } else if (head_dim == 256 && !decode) {
+    launch_attn<256, false>(p, num_work, stream);
   } else {
     throw std::invalid_argument("paged_attention: unsupported head_dim " +
                                 std::to_string(head_dim));
@@ -437,6 +439,9 @@ void paged_attention_launch(const PagedAttnParams& p, int num_work, int head_dim
     dim3 grid(p.total_tokens, p.Hq);
     if (head_dim == 128)
       launch_pdl(attn_combine_kernel<128>, grid, dim3(128), 0, stream, (const float*)p.part_o,
+                 (const float*)p.part_lse, p.out, p.o_stride_t, p.total_tokens, p.Hq, p.num_splits);
+    else if (head_dim == 256)
+      launch_pdl(attn_combine_kernel<256>, grid, dim3(256), 0, stream, (const float*)p.part_o,
                  (const float*)p.part_lse, p.out, p.o_stride_t, p.total_tokens, p.Hq, p.num_splits);
     else
       launch_pdl(attn_combine_kernel<64>, grid, dim3(64), 0, stream, (const float*)p.part_o,

@@ -39,7 +39,6 @@ namespace b200 {
 namespace {
 
 constexpr int kTok = 16;  // tokens per tile (= rows of one TMA box)
-constexpr int kWarps = 8;
 constexpr float kLog2eDec = 1.4426950408889634f;
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
@@ -105,7 +104,7 @@ __device__ __forceinline__ Unit unit_info(const PagedAttnParams& p, int u) {
 
 }  // namespace
 
-template <int D, int STAGES>
+template <int D, int STAGES, int kWarps>
 __global__ void __launch_bounds__(kWarps * 32, 1)
     paged_decode_kernel(const __grid_constant__ CUtensorMap tk,
                         const __grid_constant__ CUtensorMap tv, const PagedAttnParams p,
@@ -387,32 +386,38 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
 }
 
 namespace {
+// Per head dim: warps per CTA and ring stages per warp (16-token K+V stages of 64 * D bytes),
+// sized so the rings fill ~192 KB of shared memory with one CTA per SM.
 template <int D>
-constexpr int decode_stages() {
-  return D == 64 ? 6 : 3;
-}
-template <int D>
-constexpr int decode_smem() {
-  constexpr int st = decode_stages<D>();
-  return kWarps * st * 2 * kTok * D * 2 + kWarps * st * 8 + kWarps * (st + 2) * 4 + 1024;
-}
+struct DecodeCfg {
+  static constexpr int warps = D == 256 ? 4 : 8;
+  static constexpr int stages = D == 64 ? 6 : 3;
+  static constexpr int smem =
+      warps * stages * 2 * kTok * D * 2 + warps * stages * 8 + warps * (stages + 2) * 4 + 1024;
+};
 }  // namespace
 
-int paged_decode_warps_per_cta() { return kWarps; }
+int paged_decode_warps_per_cta(int head_dim) {
+  return head_dim == 256 ? DecodeCfg<256>::warps : DecodeCfg<128>::warps;
+}
 
 template <int D>
 static void launch_decode(const CUtensorMap& tk, const CUtensorMap& tv, const PagedAttnParams& p,
-                          int num_units, int grid, cudaStream_t stream) {
-  constexpr int smem = decode_smem<D>();
-  static_assert(smem <= 227 * 1024, "decode ring exceeds shared memory");
-  auto kern = paged_decode_kernel<D, decode_stages<D>()>;
+                          int num_units, cudaStream_t stream) {
+  using C = DecodeCfg<D>;
+  static_assert(C::smem <= 227 * 1024, "decode ring exceeds shared memory");
+  auto kern = paged_decode_kernel<D, C::stages, C::warps>;
   static std::atomic<uint64_t> configured{0};
-  set_max_dynamic_smem_once(kern, smem, configured);
-  launch_pdl(kern, dim3(grid), dim3(kWarps * 32), smem, stream, tk, tv, p, num_units);
+  set_max_dynamic_smem_once(kern, C::smem, configured);
+  int grid = num_sms_cached();
+  const int need = (num_units + C::warps - 1) / C::warps;
+  if (need < grid) grid = need;
+  launch_pdl(kern, dim3(grid), dim3(C::warps * 32), C::smem, stream, tk, tv, p, num_units);
 }
 
 bool paged_decode_tma_supported(const PagedAttnParams& p, int head_dim) {
-  return p.kv_rows > 0 && p.sched != nullptr && (head_dim == 64 || head_dim == 128) &&
+  return p.kv_rows > 0 && p.sched != nullptr &&
+         (head_dim == 64 || head_dim == 128 || head_dim == 256) &&
          p.block_size % kTok == 0 &&
          p.kv_block_stride == (long long)p.Hkv * p.block_size * head_dim &&
          (reinterpret_cast<uintptr_t>(p.k_cache) & 15) == 0 &&
@@ -426,13 +431,12 @@ void paged_decode_tma_launch(const PagedAttnParams& p, int num_work, int head_di
   const CUtensorMap tv =
       make_tmap_bf16_2d(p.v_cache, head_dim, (uint64_t)p.kv_rows, head_dim, 64, kTok, true);
   const int num_units = num_work * p.Hkv * p.num_splits;
-  int grid = num_sms_cached();
-  const int need = (num_units + kWarps - 1) / kWarps;
-  if (need < grid) grid = need;
   if (head_dim == 128)
-    launch_decode<128>(tk, tv, p, num_units, grid, stream);
+    launch_decode<128>(tk, tv, p, num_units, stream);
+  else if (head_dim == 256)
+    launch_decode<256>(tk, tv, p, num_units, stream);
   else
-    launch_decode<64>(tk, tv, p, num_units, grid, stream);
+    launch_decode<64>(tk, tv, p, num_units, stream);
 }
 
 }  // namespace b200

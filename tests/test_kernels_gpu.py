@@ -94,14 +94,14 @@ def _make_batch(device, q_lens, ctx_lens, Hq, Hkv, D, bs=16, num_blocks=None, se
     return q, k_cache, v_cache, bt.to(device), torch.tensor(seq_lens, dtype=torch.int32).to(device), q_start.to(device)
 
 
-@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("D", [64, 128, 256])
 @pytest.mark.parametrize("bs", [16, 32])
 @pytest.mark.parametrize("q_len", [1, 3])
 @pytest.mark.parametrize("window,sinks", [(0, False), (100, True)])
 def test_paged_decode_tma(cuda_device, D, bs, q_len, window, sinks):
     """Decode batches run the persistent TMA kernel (contiguous caches, block_size % 16 == 0);
     several split factors, including splits that are empty for short sequences."""
-    Hq, Hkv = (16, 4) if D == 128 else (20, 4)
+    Hq, Hkv = {128: (16, 4), 64: (20, 4), 256: (8, 2)}[D]
     ctx = [1, 15, 16, 17, 63, 64, 65, 300, 1000, 2047, 5]
     q_lens = [q_len] * len(ctx)
     q, kc, vc, bt, sl, qs = _make_batch(cuda_device, q_lens, ctx, Hq, Hkv, D, bs=bs)
@@ -118,11 +118,11 @@ def test_paged_decode_tma(cuda_device, D, bs, q_len, window, sinks):
             assert _rel_err(out, ref) < 2e-2, splits
 
 
-@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("D", [64, 128, 256])
 @pytest.mark.parametrize("case", ["prefill", "decode", "mixed", "chunked"])
 @pytest.mark.parametrize("window,sinks", [(0, False), (128, True), (0, True)])
 def test_paged_attention(cuda_device, D, case, window, sinks):
-    Hq, Hkv = (8, 2) if D == 128 else (16, 2)
+    Hq, Hkv = {128: (8, 2), 64: (16, 2), 256: (8, 2)}[D]
     if case == "prefill":
         q_lens, ctx = [100, 1, 257, 64], [0, 0, 0, 0]
     elif case == "decode":

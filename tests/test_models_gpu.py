@@ -46,3 +46,40 @@ def _agree(d, **kw):
 
 def test_gpt_oss_gpu_matches_cpu(cuda_device):
     _agree(_gpt_oss_ckpt())
+
+
+def _hybrid_ckpt():
+    from transformers import Qwen3_5MoeForCausalLM
+    from transformers.models.qwen3_5_moe.configuration_qwen3_5_moe import Qwen3_5MoeTextConfig
+
+    torch.manual_seed(0)
+    cfg = Qwen3_5MoeTextConfig(hidden_size=256, num_hidden_layers=4, num_attention_heads=4, num_key_value_heads=2,
+                               head_dim=256, linear_key_head_dim=128, linear_value_head_dim=128,
+                               linear_num_key_heads=2, linear_num_value_heads=4, linear_conv_kernel_dim=4,
+                               moe_intermediate_size=128, shared_expert_intermediate_size=128, num_experts=16,
+                               num_experts_per_tok=4, vocab_size=1024, max_position_embeddings=1024,
+                               initializer_range=0.05, tie_word_embeddings=False,
+                               rope_parameters={"rope_type": "default", "rope_theta": 10000.0,
+                                                "partial_rotary_factor": 0.25})
+    hf = Qwen3_5MoeForCausalLM(cfg).to(torch.bfloat16).eval()
+    d = tempfile.mkdtemp(prefix="hybrid_gpu_")
+    hf.save_pretrained(d, safe_serialization=True)
+    return d
+
+
+def test_hybrid_gpu_matches_cpu(cuda_device):
+    _agree(_hybrid_ckpt())
+
+
+def test_qwen3_moe_gpu_matches_cpu(cuda_device):
+    from transformers import Qwen3MoeConfig, Qwen3MoeForCausalLM
+
+    torch.manual_seed(0)
+    cfg = Qwen3MoeConfig(hidden_size=256, num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
+                         head_dim=64, intermediate_size=512, moe_intermediate_size=128, num_experts=16,
+                         num_experts_per_tok=4, norm_topk_prob=True, vocab_size=1024,
+                         max_position_embeddings=1024, initializer_range=0.05)
+    hf = Qwen3MoeForCausalLM(cfg).to(torch.bfloat16).eval()
+    d = tempfile.mkdtemp(prefix="qwen3moe_gpu_")
+    hf.save_pretrained(d, safe_serialization=True)
+    _agree(d)

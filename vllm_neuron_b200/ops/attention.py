@@ -55,7 +55,7 @@ def build_work(q_lens: np.ndarray, seq_lens: np.ndarray, group: int, num_kv_head
         # csrc/attn/paged_decode.cu: persistent warps (DECODE_WARPS per SM) claim
         # (sequence, KV head, split) units.  Aim for ~3 units per warp for load balance, but
         # keep at least 4 tiles (64 tokens) per split so the per-unit cost stays amortised.
-        warps = num_sms * DECODE_WARPS
+        warps = num_sms * (DECODE_WARPS // 2 if head_dim == 256 else DECODE_WARPS)
         splits = max(1, min(max_splits, math.ceil(3 * warps / max(1, units)),
                             max(1, max_len // (4 * DECODE_TILE))))
         return AttnWork(work.astype(np.int32), True, splits)
