@@ -1,5 +1,6 @@
 """Host-side units: config parsing, block manager, scheduler policy, group rank math."""
 import pytest
+import torch
 
 from vllm_neuron_b200.config import B200Config, ModelArchConfig
 from vllm_neuron_b200.engine.block_manager import BlockManager
@@ -119,3 +120,18 @@ def test_emulated_rank_engine_runs_on_cpu():
     eng.add_request(list(range(10)), SamplingParams(temperature=0.0, max_tokens=3, ignore_eos=True))
     done = eng.run_until_done()
     assert len(done) == 1 and len(done[0].output_token_ids) == 3
+
+
+def test_prompt_logits_matches_hf():
+    """The logit-validation hook returns the HF logits of the last prompt position."""
+    from tests._tiny import random_prompts, tiny_llama_checkpoint
+    from vllm_neuron_b200.entrypoints import LLM
+
+    d, hf = tiny_llama_checkpoint()
+    prompts = random_prompts(n=2, length=20)
+    llm = LLM(d, device="cpu", dtype="float32", max_num_seqs=4, max_model_len=128, num_gpu_blocks=32,
+              max_num_batched_tokens=128)
+    got = llm.engine.prompt_logits(prompts)
+    with torch.no_grad():
+        ref = torch.stack([hf(torch.tensor([p])).logits[0, -1] for p in prompts])
+    assert torch.allclose(got, ref, atol=1e-4, rtol=1e-4)

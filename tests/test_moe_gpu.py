@@ -59,14 +59,14 @@ def test_moe_block(cuda_device, T, kind):
     b_dn = (torch.randn(e_local, H, device=cuda_device, generator=g) * 0.1).to(torch.bfloat16) if biases else None
     ws = M.MoEWorkspace.create(512, k, E, e_local, H, I, cuda_device)
     out = M.moe_block(x, rw, w_gu, w_dn, k, mode, True, rb, b_gu, b_dn, act, e_start=e_start, ws=ws)
-    logits = ws.logits[:T]
+    logits = ws.logits[:T, :E]
     ids, w = M.route_ref(logits, k, mode, True, rb)
     ref = M.experts_ref(x, ids, w, w_gu, w_dn, b_gu, b_dn, act, e_start=e_start)
     assert _rel_err(out, ref) < 2e-2
     # a second call with other tokens reuses the workspace
     x2 = torch.randn(T, H, device=cuda_device, generator=g).to(torch.bfloat16)
     out2 = M.moe_block(x2, rw, w_gu, w_dn, k, mode, True, rb, b_gu, b_dn, act, e_start=e_start, ws=ws)
-    ids2, w2 = M.route_ref(ws.logits[:T], k, mode, True, rb)
+    ids2, w2 = M.route_ref(ws.logits[:T, :E], k, mode, True, rb)
     ref2 = M.experts_ref(x2, ids2, w2, w_gu, w_dn, b_gu, b_dn, act, e_start=e_start)
     assert _rel_err(out2, ref2) < 2e-2
 

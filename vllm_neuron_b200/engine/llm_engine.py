@@ -161,6 +161,31 @@ class LLMEngine:
             raise RuntimeError(f"device status {code}: a bounded wait of a fused collective expired "
                                "(a peer rank stopped or fell out of step)")
 
+    @torch.no_grad()
+    def prompt_logits(self, prompts: list[list[int]]) -> torch.Tensor:
+        """Logits of the last prompt position of each prompt (one prefill step, nothing is
+        sampled or kept): the hook of the logit-validation tooling.  Returns ``[N, V]`` fp32 on
+        the CPU.  Must be called with no requests in flight."""
+        from .scheduler import ScheduledRequest, SchedulerOutput
+
+        if self.has_unfinished_requests():
+            raise RuntimeError("prompt_logits needs an idle engine")
+        reqs = []
+        try:
+            for i, p in enumerate(prompts):
+                r = Request(f"logits-{i}", list(p), SamplingParams(max_tokens=1))
+                r.slot = self._free_slots.pop()
+                if not self.block_manager.allocate(r, len(p)):
+                    raise RuntimeError("not enough KV blocks for prompt_logits")
+                reqs.append(r)
+            out = SchedulerOutput([ScheduledRequest(r, 0, r.num_prompt_tokens, True) for r in reqs],
+                                  sum(r.num_prompt_tokens for r in reqs))
+            return self.runner.forward_logits(out).float().cpu()
+        finally:
+            for r in reqs:
+                self.block_manager.free_request(r)
+                self._free_slots.append(r.slot)
+
     def has_unfinished_requests(self) -> bool:
         return self.scheduler.has_unfinished() or self._inflight is not None
 

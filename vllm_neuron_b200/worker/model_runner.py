@@ -370,6 +370,27 @@ class ModelRunner:
             ev.record()
         return StepHandle(ev, tok_host, lps, S)
 
+    @torch.no_grad()
+    def forward_logits(self, out: SchedulerOutput) -> torch.Tensor:
+        """Run one step eagerly and return the full-vocabulary logits of its sampling rows
+        (``[S, V]``, model dtype) instead of sampling (logit validation / accuracy tooling)."""
+        B = len(out.scheduled)
+        S = sum(1 for s in out.scheduled if s.samples)
+        self._buf_idx ^= 1
+        self.host_buf = self.host_bufs[self._buf_idx]
+        self.host_np = self.host_buf.numpy()
+        lay = Layout(out.num_tokens, B, S, self._max_work_for(out), self.max_blocks)
+        _, decode, splits = self._pack(out, lay)
+        W = self._last_work_len
+        dev = self.dev_buf[:lay.total]
+        dev.copy_(self.host_buf[:lay.total], non_blocking=self.is_cuda)
+        fb, _ = self._views(dev, lay, B, S, W, decode, splits)
+        fb.work = fb.work[:W]
+        logits = self.model.forward(fb).clone()
+        if self.is_cuda:
+            torch.cuda.synchronize(self.device)
+        return logits
+
     def execute(self, out: SchedulerOutput, want_logprobs: bool = False) -> tuple[np.ndarray, np.ndarray | None]:
         """Run one step synchronously; returns sampled tokens (and logprobs) in row order."""
         return self.launch(out, want_logprobs).result()
