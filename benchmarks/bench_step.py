@@ -21,7 +21,7 @@ import torch
 
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
-from bench import LLAMA3_8B  # noqa: E402
+from benchmarks.bench_serving import MODELS  # noqa: E402
 from vllm_neuron_b200.engine.request import Request  # noqa: E402
 from vllm_neuron_b200.engine.sampling_params import SamplingParams  # noqa: E402
 from vllm_neuron_b200.engine.scheduler import ScheduledRequest, SchedulerOutput  # noqa: E402
@@ -30,6 +30,7 @@ from vllm_neuron_b200.entrypoints import LLM  # noqa: E402
 
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--model", default="llama3-8b", choices=sorted(MODELS))
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--ctx", type=int, default=1152)
     ap.add_argument("--chunk", type=int, default=8192)
@@ -48,7 +49,9 @@ def main():
     rank, world = ps.init_distributed(timeout_s=300)
     if world > 1:
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
-    cfg = dict(LLAMA3_8B, num_hidden_layers=a.layers)
+    cfg = dict(MODELS[a.model]["cfg"], num_hidden_layers=a.layers)
+    if "layer_types" in cfg:
+        cfg["layer_types"] = cfg["layer_types"][:a.layers]
     B, L = a.batch, a.ctx
     max_len = max(L + 64, 2048)
     blocks = B * (max_len // 16 + 1) + 64
@@ -74,6 +77,7 @@ def main():
         r = Request(str(i), list(np.random.randint(0, 1000, L)), sp)
         r.output_token_ids = [1]
         r.num_computed_tokens = L
+        r.slot = i
         r.block_ids = list(range(1 + i * nb, 1 + (i + 1) * nb))
         reqs.append(r)
     out = SchedulerOutput([ScheduledRequest(r, L, 1, True) for r in reqs], B)
@@ -96,6 +100,7 @@ def main():
         preqs = []
         for i in range(n_seq):
             r = Request("p%d" % i, list(np.random.randint(0, 1000, per)), sp)
+            r.slot = B + i
             r.block_ids = list(range(1 + i * nb2, 1 + (i + 1) * nb2))
             preqs.append(r)
         pout = SchedulerOutput([ScheduledRequest(r, 0, per, True) for r in preqs], per * n_seq)
@@ -135,6 +140,7 @@ def main():
     nb2 = (per + 15) // 16
     for i in range(n_seq):
         r = Request("p%d" % i, list(np.random.randint(0, 1000, per)), sp)
+        r.slot = B + i
         r.block_ids = list(range(1 + i * nb2, 1 + (i + 1) * nb2))
         preqs.append(r)
     pout = SchedulerOutput([ScheduledRequest(r, 0, per, True) for r in preqs], per * n_seq)
@@ -147,7 +153,7 @@ def main():
     torch.cuda.synchronize()
     res["prefill_chunk_ms"] = e0.elapsed_time(e1) / 3
     res["prefill_tokens"] = per * n_seq
-    flops = 2 * 7.5e9 * per * n_seq * a.layers / 32
+    flops = 2 * 7.5e9 * per * n_seq * a.layers / 32  # Llama-3-8B dense FLOPs (other models: ignore)
     res["prefill_tflops_dense_only"] = flops / (res["prefill_chunk_ms"] * 1e9)
     res.update(batch=B, ctx=L, layers=a.layers, tp=world, emulated_tp=a.emulate_tp)
     if world > 1:
