@@ -16,8 +16,9 @@
 //   gated_delta_rule   one CTA (256 threads) per (sequence, value head); thread (v, half) keeps
 //                      column v, rows [64 * half, 64 * half + 64) of S in registers; per token
 //                      two k-reductions go through shared memory; the gated RMSNorm over dv is
-//                      a CTA reduction.  Tokens are processed in order (the recurrence); the
-//                      work is spread over sequences x heads.
+//                      a CTA reduction.  Tokens are processed in order (the recurrence), with
+//                      the next token's inputs prefetched; the work is spread over
+//                      sequences x heads.
 #include <cuda_bf16.h>
 
 #include <stdexcept>
@@ -76,15 +77,17 @@ __global__ void __launch_bounds__(128) causal_conv1d_kernel(
   for (int j = 0; j < K - 1; ++j) st[j] = __float2bfloat16(win[j]);
 }
 
-// dk = dv = 128, 256 threads.
+// dk = dv = 128, 256 threads.  The inputs of token i + 1 are loaded while token i is
+// processed (they do not depend on the state), and the shared-memory exchanges use separate
+// buffers per phase so one token costs five CTA barriers.
 __global__ void __launch_bounds__(256) gated_delta_rule_kernel(const GatedDeltaParams p,
                                                                 LinearAttnBatch bt) {
   constexpr int DK = 128, DV = 128, R = 64;  // rows of S per thread
   pdl_trigger();
   pdl_wait();
   __shared__ float qs[DK], ks[DK];
-  __shared__ float red[2][DV];
-  __shared__ float wsum[8];
+  __shared__ float red_kv[2][DV], red_o[2][DV];
+  __shared__ float wsum_qk[8], wsum_o[8];
   const int b = blockIdx.x;
   const int h = blockIdx.y;
   const int tid = threadIdx.x;
@@ -103,64 +106,69 @@ __global__ void __launch_bounds__(256) gated_delta_rule_kernel(const GatedDeltaP
   const float nw = __bfloat162float(p.norm_w[v]);
   const float qscale = rsqrtf((float)DK);
   const int warp = tid >> 5, lane = tid & 31;
+  const int d = tid & (DK - 1);
+  const long long qk_off = (half ? p.Hk * DK : 0) + (long long)kh * DK + d;
+  const long long v_off = 2 * p.Hk * DK + (long long)h * DV + v;
+  const long long z_off = (long long)h * DV + v;
+
+  // per-token inputs of this thread: its q or k element, v element, z element, a, b
+  float n_qk = 0.f, n_v = 0.f, n_z = 0.f, n_a = 0.f, n_b = 0.f;
+  auto load = [&](long long t) {
+    n_qk = __bfloat162float(p.qkv[t * p.ld_qkv + qk_off]);
+    n_v = __bfloat162float(p.qkv[t * p.ld_qkv + v_off]);
+    n_z = half == 0 ? __bfloat162float(p.z[t * p.ld_zab + z_off]) : 0.f;
+    n_a = __bfloat162float(p.a[t * p.ld_zab + h]);
+    n_b = __bfloat162float(p.b[t * p.ld_zab + h]);
+  };
+  if (n > 0) load(t0);
 
   for (int i = 0; i < n; ++i) {
     const long long t = t0 + i;
+    const float val = n_qk, vt = n_v, zt = n_z, a = n_a, bb = n_b;
+    if (i + 1 < n) load(t + 1);
     // q (threads 0..127) and k (threads 128..255), l2-normalised over dk
+    const float ss = warp_sum(val * val);
+    if (lane == 0) wsum_qk[warp] = ss;
+    __syncthreads();  // A
     {
-      const int d = tid & (DK - 1);
-      const __nv_bfloat16* src = p.qkv + t * p.ld_qkv + (half ? p.Hk * DK : 0) + (long long)kh * DK;
-      const float val = __bfloat162float(src[d]);
-      float ss = warp_sum(val * val);
-      if (lane == 0) wsum[warp] = ss;
-      __syncthreads();
-      const float tot = half ? wsum[4] + wsum[5] + wsum[6] + wsum[7] : wsum[0] + wsum[1] + wsum[2] + wsum[3];
+      const float tot = half ? wsum_qk[4] + wsum_qk[5] + wsum_qk[6] + wsum_qk[7]
+                             : wsum_qk[0] + wsum_qk[1] + wsum_qk[2] + wsum_qk[3];
       const float inv = rsqrtf(tot + 1e-6f);
       if (half) ks[d] = val * inv;
       else qs[d] = val * inv * qscale;
     }
-    const float a = __bfloat162float(p.a[t * p.ld_zab + h]);
-    const float bb = __bfloat162float(p.b[t * p.ld_zab + h]);
     const float g = __expf(A * softplus_d(a + dtb));
     const float beta = 1.f / (1.f + __expf(-bb));
-    const float vt = __bfloat162float(p.qkv[t * p.ld_qkv + 2 * p.Hk * DK + (long long)h * DV + v]);
-    __syncthreads();
-    // decay and k-projection of the state
+    __syncthreads();  // B
     float kv = 0.f;
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       s[r] *= g;
       kv += s[r] * ks[half * R + r];
     }
-    red[half][v] = kv;
-    __syncthreads();
-    const float delta = (vt - (red[0][v] + red[1][v])) * beta;
+    red_kv[half][v] = kv;
+    __syncthreads();  // C
+    const float delta = (vt - (red_kv[0][v] + red_kv[1][v])) * beta;
     float o = 0.f;
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       s[r] += ks[half * R + r] * delta;
       o += s[r] * qs[half * R + r];
     }
-    __syncthreads();  // red[] reads above are done
-    red[half][v] = o;
-    __syncthreads();
-    // gated RMSNorm over dv (threads of half 0 hold the outputs)
-    // the recurrence output is rounded to the activation dtype before the norm
-    const float ov = __bfloat162float(__float2bfloat16(red[0][v] + red[1][v]));
-    float sq = half == 0 ? ov * ov : 0.f;
-    sq = warp_sum(sq);
-    __syncthreads();  // wsum reuse
-    if (lane == 0) wsum[warp] = sq;
-    __syncthreads();
+    red_o[half][v] = o;
+    __syncthreads();  // E
+    // the recurrence output is rounded to the activation dtype before the gated RMSNorm
+    const float ov = __bfloat162float(__float2bfloat16(red_o[0][v] + red_o[1][v]));
+    const float sq = warp_sum(half == 0 ? ov * ov : 0.f);
+    if (lane == 0) wsum_o[warp] = sq;
+    __syncthreads();  // F
     if (half == 0) {
-      const float tot = wsum[0] + wsum[1] + wsum[2] + wsum[3];
+      const float tot = wsum_o[0] + wsum_o[1] + wsum_o[2] + wsum_o[3];
       const float rstd = rsqrtf(tot / (float)DV + p.eps);
-      const float zt = __bfloat162float(p.z[t * p.ld_zab + (long long)h * DV + v]);
       // reference order: normalise, cast, scale by the weight, then multiply by silu(z)
       const float nrm = __bfloat162float(__float2bfloat16(ov * rstd));
       p.out[t * p.ld_out + (long long)h * DV + v] = __float2bfloat16(nw * nrm * silu_d(zt));
     }
-    __syncthreads();
   }
 #pragma unroll
   for (int r = 0; r < R; ++r) S[(long long)(half * R + r) * DV + v] = s[r];

@@ -149,20 +149,40 @@ __global__ void __launch_bounds__(1024) moe_align_kernel(const int* __restrict__
     if (e >= 0 && e < e_local) atomicAdd(&cnt[e], 1);
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int run = 0, nt = 0;
-    for (int e = 0; e < e_local; ++e) {
-      offsets[e] = run;
-      const int c = cnt[e];
-      for (int r = 0; r < c; r += 128) {
-        if (nt < gmax) gtiles[nt] = make_int4(e, run + r, run + c, 0);
-        ++nt;
+  // Exclusive scans of the row counts and of the 128-row tile counts, 32 experts at a time
+  // by warp 0 (carry kept in lane registers).
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    int row_carry = 0, tile_carry = 0;
+    for (int e0 = 0; e0 < e_local; e0 += 32) {
+      const int e = e0 + lane;
+      const int c = e < e_local ? cnt[e] : 0;
+      const int nt = (c + 127) / 128;
+      int rs = c, ts = nt;  // inclusive scans
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int r2 = __shfl_up_sync(0xffffffffu, rs, o);
+        const int t2 = __shfl_up_sync(0xffffffffu, ts, o);
+        if (lane >= o) {
+          rs += r2;
+          ts += t2;
+        }
       }
-      cur[e] = run;
-      run += c;
+      const int row0 = row_carry + rs - c;
+      const int tile0 = tile_carry + ts - nt;
+      if (e < e_local) {
+        offsets[e] = row0;
+        cur[e] = row0;
+        for (int r = 0; r < nt; ++r)
+          if (tile0 + r < gmax) gtiles[tile0 + r] = make_int4(e, row0 + 128 * r, row0 + c, 0);
+      }
+      row_carry += __shfl_sync(0xffffffffu, rs, 31);
+      tile_carry += __shfl_sync(0xffffffffu, ts, 31);
     }
-    offsets[e_local] = run;
-    *gcount = nt < gmax ? nt : gmax;
+    if (lane == 0) {
+      offsets[e_local] = row_carry;
+      *gcount = tile_carry < gmax ? tile_carry : gmax;
+    }
   }
   __syncthreads();
   for (int i = threadIdx.x; i < n_assign; i += blockDim.x) {
@@ -204,23 +224,51 @@ __global__ void moe_act_kernel(const __nv_bfloat16* __restrict__ gu,
   const __nv_bfloat16* g = gu + (long long)r * 2 * I;
   const __nv_bfloat16* u = g + I;
   const __nv_bfloat16* bg = bias != nullptr ? bias + (long long)row_expert[r] * 2 * I : nullptr;
-  for (int j = threadIdx.x; j < I; j += blockDim.x) {
-    float a = __bfloat162float(g[j]);
-    float b = __bfloat162float(u[j]);
-    if (bg != nullptr) {
-      // the projection (+ bias) is rounded to bf16 like the reference's bf16 linear
-      a = __bfloat162float(__float2bfloat16(a + __bfloat162float(bg[j])));
-      b = __bfloat162float(__float2bfloat16(b + __bfloat162float(bg[I + j])));
-    }
-    float y;
+  auto act = [&](float a, float b) {
     if (mode == MOE_ACT_GPTOSS) {
       a = fminf(a, limit);
       b = fminf(fmaxf(b, -limit), limit);
-      y = (b + 1.f) * (a / (1.f + __expf(-alpha * a)));
-    } else {
-      y = a / (1.f + __expf(-a)) * b;
+      return (b + 1.f) * (a / (1.f + __expf(-alpha * a)));
     }
-    out[(long long)r * I + j] = __float2bfloat16(y);
+    return a / (1.f + __expf(-a)) * b;
+  };
+  const bool vec = (I % 8) == 0;
+  for (int j = threadIdx.x * (vec ? 8 : 1); j < I; j += blockDim.x * (vec ? 8 : 1)) {
+    const int n = vec ? 8 : 1;
+    float a[8], b[8];
+    if (vec) {
+      const uint4 ga = *reinterpret_cast<const uint4*>(g + j);
+      const uint4 ub = *reinterpret_cast<const uint4*>(u + j);
+      const uint32_t gw[4] = {ga.x, ga.y, ga.z, ga.w}, uw[4] = {ub.x, ub.y, ub.z, ub.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 fg = unpack_bf16x2(gw[q]), fu = unpack_bf16x2(uw[q]);
+        a[2 * q] = fg.x;
+        a[2 * q + 1] = fg.y;
+        b[2 * q] = fu.x;
+        b[2 * q + 1] = fu.y;
+      }
+    } else {
+      a[0] = __bfloat162float(g[j]);
+      b[0] = __bfloat162float(u[j]);
+    }
+    float y[8];
+    for (int q = 0; q < n; ++q) {
+      float av = a[q], bv = b[q];
+      if (bg != nullptr) {
+        // the projection (+ bias) is rounded to bf16 like the reference's bf16 linear
+        av = __bfloat162float(__float2bfloat16(av + __bfloat162float(bg[j + q])));
+        bv = __bfloat162float(__float2bfloat16(bv + __bfloat162float(bg[I + j + q])));
+      }
+      y[q] = act(av, bv);
+    }
+    __nv_bfloat16* o = out + (long long)r * I + j;
+    if (vec) {
+      *reinterpret_cast<uint4*>(o) = make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]),
+                                                pack_bf16x2(y[4], y[5]), pack_bf16x2(y[6], y[7]));
+    } else {
+      o[0] = __float2bfloat16(y[0]);
+    }
   }
 }
 
@@ -235,20 +283,52 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y,
   pdl_wait();
   const int t = blockIdx.x;
   const float sg = shared != nullptr ? (shared_gate != nullptr ? shared_gate[t] : 1.f) : 0.f;
-  for (int c = threadIdx.x; c < H; c += blockDim.x) {
-    float acc = 0.f;
-    if (shared != nullptr) acc = sg * __bfloat162float(shared[(long long)t * ld_shared + c]);
+  // 8 columns per thread, 16-byte loads (H % 8 == 0)
+  for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
+    float acc[8];
+    if (shared != nullptr) {
+      const uint4 u = *reinterpret_cast<const uint4*>(shared + (long long)t * ld_shared + c);
+      const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = unpack_bf16x2(w4[q]);
+        acc[2 * q] = sg * f.x;
+        acc[2 * q + 1] = sg * f.y;
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) acc[q] = 0.f;
+    }
     for (int j = 0; j < k; ++j) {
       const int pos = inv_pos[(long long)t * k + j];
       if (pos < 0) continue;
-      float v = __bfloat162float(y[(long long)pos * H + c]);
+      const float wt = weights[(long long)t * k + j];
+      const uint4 u = *reinterpret_cast<const uint4*>(y + (long long)pos * H + c);
+      const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+      float v[8];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = unpack_bf16x2(w4[q]);
+        v[2 * q] = f.x;
+        v[2 * q + 1] = f.y;
+      }
       if (bias != nullptr) {
         const int e = ids[(long long)t * k + j] - e_start;
-        v = __bfloat162float(__float2bfloat16(v + __bfloat162float(bias[(long long)e * H + c])));
+        const uint4 bu = *reinterpret_cast<const uint4*>(bias + (long long)e * H + c);
+        const uint32_t b4[4] = {bu.x, bu.y, bu.z, bu.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = unpack_bf16x2(b4[q]);
+          v[2 * q] = __bfloat162float(__float2bfloat16(v[2 * q] + f.x));
+          v[2 * q + 1] = __bfloat162float(__float2bfloat16(v[2 * q + 1] + f.y));
+        }
       }
-      acc += weights[(long long)t * k + j] * v;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) acc[q] += wt * v[q];
     }
-    out[(long long)t * ldo + c] = __float2bfloat16(acc);
+    *reinterpret_cast<uint4*>(out + (long long)t * ldo + c) =
+        make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
+                   pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
   }
 }
 
@@ -295,6 +375,8 @@ void moe_combine_launch(const __nv_bfloat16* y, const int* inv_pos, const float*
                         const float* shared_gate, __nv_bfloat16* out, long long ldo,
                         cudaStream_t s) {
   if (T == 0) return;
+  if (H % 8 != 0 || ldo % 8 != 0 || (shared != nullptr && ld_shared % 8 != 0))
+    throw std::invalid_argument("moe_combine: hidden size and strides must be multiples of 8");
   launch_pdl(moe_combine_kernel, dim3(T), dim3(256), 0, s, y, inv_pos, weights, ids, bias, e_start,
              k, H, shared, ld_shared, shared_gate, out, ldo);
 }
