@@ -1,0 +1,62 @@
+"""Speculative decoding on CPU: whatever the proposer drafts, greedy output must equal plain
+greedy decoding (the target model verifies every token); the n-gram proposer and the
+rejection sampler are checked against small oracles."""
+import torch
+
+from tests._tiny import random_prompts, tiny_llama_checkpoint
+from vllm_neuron_b200.engine.sampling_params import SamplingParams
+from vllm_neuron_b200.entrypoints import LLM
+from vllm_neuron_b200.spec_decode import NgramProposer, rejection_sample, rejection_sample_ref
+
+
+def test_ngram_proposer():
+    p = NgramProposer(3, 1, 3)
+    assert p.propose_one([1, 2, 3, 9, 1, 2, 3]) == [9, 1, 2]
+    assert p.propose_one([5, 6, 7]) == []
+    assert p.propose_one([4, 4, 4, 4]) == [4]
+
+
+def test_rejection_sampler_greedy_matches_oracle():
+    torch.manual_seed(0)
+    drafts = [[3, 1, 4], [2], [], [7, 7]]
+    n = sum(len(d) + 1 for d in drafts)
+    logits = torch.randn(n, 10)
+    am = logits.argmax(-1).tolist()
+    # force some acceptances
+    logits[0, 3] = 10
+    logits[1, 1] = 10
+    am = logits.argmax(-1).tolist()
+    rows, r = [], 0
+    for d in drafts:
+        rows.append(am[r:r + len(d) + 1])
+        r += len(d) + 1
+    got = rejection_sample(logits, drafts, [0.0] * 4)
+    assert got == rejection_sample_ref(rows, drafts)
+    assert got[0][:2] == [3, 1]
+
+
+def test_rejection_sampler_random_keeps_target_distribution():
+    # one draft token, target p over 4 tokens: P(output = t) must equal p(t)
+    p = torch.tensor([0.1, 0.2, 0.3, 0.4])
+    logits = torch.log(p).repeat(2, 1)
+    g = torch.Generator().manual_seed(0)
+    counts = torch.zeros(4)
+    for _ in range(4000):
+        counts[rejection_sample(logits, [[2]], [1.0], [g])[0][0]] += 1
+    assert torch.allclose(counts / counts.sum(), p, atol=0.03)
+
+
+def test_ngram_spec_decode_matches_greedy():
+    d, _ = tiny_llama_checkpoint()
+    # prompts with repetition so the n-gram proposer finds drafts
+    base = random_prompts(n=3, length=12)
+    prompts = [b + b + b[:6] for b in base]
+    sp = SamplingParams(temperature=0, max_tokens=16, ignore_eos=True)
+    kw = dict(device="cpu", dtype="float32", max_num_seqs=4, max_model_len=256, num_gpu_blocks=64,
+              max_num_batched_tokens=64)
+    ref = LLM(d, **kw).generate(prompts, sp)
+    llm = LLM(d, speculative_config={"method": "ngram", "num_speculative_tokens": 3}, **kw)
+    got = llm.generate(prompts, sp)
+    assert [o.outputs[0].token_ids for o in got] == [o.outputs[0].token_ids for o in ref]
+    m = llm.engine.metrics
+    assert m.spec_draft_tokens > 0

@@ -40,6 +40,9 @@ class EngineArgs:
     cuda_graphs: bool = True
     async_scheduling: bool | None = None  # default: on for CUDA devices
     additional_config: dict = field(default_factory=dict)
+    # {"method": "ngram" | "eagle3", "num_speculative_tokens": k, "model": draft checkpoint,
+    #  "prompt_lookup_min"/"prompt_lookup_max": n-gram sizes}
+    speculative_config: dict | None = None
 
 
 @dataclass
@@ -126,6 +129,10 @@ class LLMEngine:
                                  else bool(args.async_scheduling))
         self._inflight = None  # (SchedulerOutput, StepHandle) of the launched, unprocessed step
         self._free_slots = list(range(self.runner.max_slots - 2, -1, -1))
+        self.proposer = None
+        if args.speculative_config:
+            self.proposer = self._make_proposer(dict(args.speculative_config))
+            self.async_scheduling = False  # drafts depend on the previous step's tokens
 
     # ---------------------------------------------------------------- requests
     def add_request(self, prompt_token_ids: list[int], params: SamplingParams | None = None,
@@ -208,9 +215,67 @@ class LLMEngine:
                 r.slot = -1
         return finished
 
+    # ---------------------------------------------------------------- speculative decoding
+    def _make_proposer(self, cfg: dict):
+        method = cfg.get("method", "ngram")
+        k = int(cfg.get("num_speculative_tokens", 3))
+        if method in ("ngram", "prompt_lookup"):
+            from ..spec_decode import NgramProposer
+
+            return NgramProposer(k, cfg.get("prompt_lookup_min", 1), cfg.get("prompt_lookup_max", 4))
+        if method in ("eagle3", "eagle"):
+            from ..spec_decode.eagle import Eagle3Proposer
+
+            return Eagle3Proposer(self, cfg, k)
+        raise ValueError(f"unknown speculative method {method!r}")
+
+    def _spec_step(self) -> list[Request]:
+        """One synchronous step with draft verification: drafts for the decoding requests, one
+        forward over [last token, drafts] (plus any prefill chunks), rejection sampling."""
+        from ..spec_decode import rejection_sample
+
+        decoding = [r for r in self.scheduler.running
+                    if r.num_pending == 0 and r.num_computed_tokens == r.num_tokens - 1]
+        props = self.proposer.propose(decoding) if decoding else {}
+        for r in decoding:
+            r.spec_token_ids = props.get(r.request_id, [])
+        out = self.scheduler.schedule()
+        for r in decoding:
+            r.spec_token_ids = []
+        if out.empty:
+            return []
+        self.num_steps += 1
+        self.metrics.steps += 1
+        logits = self.runner.forward_logits(out)
+        if hasattr(self.proposer, "observe"):
+            self.proposer.observe(out)
+        samplers = [s for s in out.scheduled if s.samples]
+        drafts = [list(s.spec) for s in samplers]
+        temps = [0.0 if s.req.sampling_params.greedy else s.req.sampling_params.temperature for s in samplers]
+        gens = []
+        for s in samplers:
+            sp = s.req.sampling_params
+            g = None
+            if not sp.greedy:
+                g = torch.Generator()
+                g.manual_seed(((sp.seed if sp.seed is not None else hash(s.req.request_id) & 0xFFFFFFFF)
+                               * 1000003 + len(s.req.output_token_ids)) & 0x7FFFFFFFFFFFFFFF)
+            gens.append(g)
+        toks = rejection_sample(logits, drafts, temps, gens)
+        self.metrics.spec_draft_tokens += sum(len(d) for d in drafts)
+        self.metrics.spec_accepted_tokens += sum(len(t) - 1 for t, d in zip(toks, drafts) if d)
+        finished = self.scheduler.update_spec(out, toks, now=time.perf_counter())
+        for req in finished:
+            if req.slot >= 0:
+                self._free_slots.append(req.slot)
+                req.slot = -1
+        return finished
+
     def step(self) -> list[Request]:
         """Schedule and launch the next step; with asynchronous scheduling the results of the
         previous step are processed while this one runs on the GPU."""
+        if self.proposer is not None:
+            return self._spec_step()
         out = self.scheduler.schedule()
         handle = None
         if not out.empty:

@@ -29,6 +29,14 @@ class ScheduledRequest:
     start: int          # first token position computed this step
     num_tokens: int     # tokens computed this step
     samples: bool       # reaches the end of the known tokens -> produces a new token
+    spec: list = field(default_factory=list)  # draft tokens verified this step (after the last token)
+
+    @property
+    def num_logits(self) -> int:
+        """Logits rows this request needs: one per verified draft plus one, or one."""
+        if not self.samples:
+            return 0
+        return len(self.spec) + 1 if self.spec else 1
 
 
 @dataclass
@@ -125,6 +133,12 @@ class Scheduler:
             if n < req.num_tokens_scheduled - req.num_computed_tokens and not self.enable_chunked_prefill:
                 i += 1
                 continue
+            spec = []
+            if n == 1 and getattr(req, "spec_token_ids", None):
+                room = min(budget - 1, self.max_model_len - req.num_tokens - 1,
+                           req.max_tokens - len(req.output_token_ids) - 1)
+                spec = list(req.spec_token_ids[:max(0, room)])
+                n += len(spec)
             ok = True
             while not self.bm.allocate(req, req.num_computed_tokens + n):
                 victim = self.running.pop()
@@ -135,7 +149,8 @@ class Scheduler:
             if not ok:
                 break
             out.scheduled.append(ScheduledRequest(req, req.num_computed_tokens, n,
-                                                  req.num_computed_tokens + n >= req.num_tokens_scheduled))
+                                                  req.num_computed_tokens + n >= req.num_tokens_scheduled,
+                                                  spec))
             scheduled_ids.add(req.request_id)
             budget -= n
             has_prefill |= is_prefill
@@ -183,6 +198,46 @@ class Scheduler:
         return out
 
     # --------------------------------------------------------------------- update
+    def update_spec(self, out: SchedulerOutput, tokens: list[list[int]],
+                    now: float | None = None) -> list[Request]:
+        """Apply a speculative step: ``tokens[i]`` are the accepted tokens (1..k+1) of the
+        i-th sampling request.  The KV of rejected drafts is dropped by rolling back
+        ``num_computed_tokens`` (their slots are rewritten by later steps)."""
+        finished = []
+        k = 0
+        for s in out.scheduled:
+            req = s.req
+            if not s.samples:
+                if not req.status.finished:
+                    self.bm.commit_full_blocks(req)
+                continue
+            toks = tokens[k]
+            k += 1
+            req.num_pending -= 1
+            if req.status.finished:
+                continue
+            if s.spec:
+                req.num_computed_tokens = s.start + len(toks)
+                req.spec_accepted = getattr(req, "spec_accepted", 0) + len(toks) - 1
+                req.spec_proposed = getattr(req, "spec_proposed", 0) + len(s.spec)
+            for tok in toks:
+                req.output_token_ids.append(int(tok))
+                if now is not None:
+                    if req.first_token_time is None:
+                        req.first_token_time = now
+                    req.token_times.append(now)
+                if req.check_stop(self.max_model_len):
+                    req.finish_time = now
+                    finished.append(req)
+                    break
+            self.bm.commit_full_blocks(req)
+        for req in finished:
+            if req in self.running:
+                self.running.remove(req)
+            self.bm.free_request(req)
+            self.requests.pop(req.request_id, None)
+        return finished
+
     def update(self, out: SchedulerOutput, sampled: list[int], logprobs: list[float] | None = None,
                now: float | None = None) -> list[Request]:
         """Apply one step's results; returns the requests that finished."""

@@ -43,7 +43,8 @@ class LLM:
                  additional_config: dict | None = None, tokenizer: str | None = None,
                  skip_tokenizer_init: bool = False, num_gpu_blocks: int | None = None,
                  enforce_eager: bool = False, device: str | None = None, dtype: str = "auto",
-                 async_scheduling: bool | None = None, **unused):
+                 async_scheduling: bool | None = None, speculative_config: dict | None = None,
+                 **unused):
         if device is None:
             device = f"cuda:{torch.cuda.current_device()}" if torch.cuda.is_available() else "cpu"
         ps.init_distributed(backend="gloo" if str(device).startswith("cpu") else None)
@@ -60,7 +61,8 @@ class LLM:
                           num_gpu_blocks=num_gpu_blocks, enable_prefix_caching=enable_prefix_caching,
                           load_format=load_format, seed=seed, dtype=dtype, device=device,
                           cuda_graphs=not enforce_eager, async_scheduling=async_scheduling,
-                          additional_config=additional_config or {})
+                          additional_config=additional_config or {},
+                          speculative_config=speculative_config)
         self.engine = LLMEngine(args, tp=st.tp)
         self.tokenizer = None
         if not skip_tokenizer_init:

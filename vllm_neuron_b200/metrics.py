@@ -44,7 +44,13 @@ class Metrics:
     padded_seqs: int = 0
     real_tokens: int = 0
     real_seqs: int = 0
+    spec_draft_tokens: int = 0      # draft tokens proposed (speculative decoding)
+    spec_accepted_tokens: int = 0   # of which accepted by the target model
     extra: dict = field(default_factory=dict)
+
+    @property
+    def spec_acceptance_rate(self) -> float:
+        return self.spec_accepted_tokens / self.spec_draft_tokens if self.spec_draft_tokens else 0.0
 
     def observe_padding(self, tokens: int, padded_tokens: int, seqs: int, padded_seqs: int):
         self.real_tokens += tokens

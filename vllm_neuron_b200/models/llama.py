@@ -281,9 +281,13 @@ class LlamaForCausalLM(torch.nn.Module):
 
     def compute_logits(self, x: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:
         S = idx.shape[0]
-        xs = self.ws_logits_x[:S]
+        if S > self.ws_logits.shape[0]:  # draft verification rows beyond the preallocated ones
+            xs = torch.empty(S, self.H, dtype=self.dtype, device=x.device)
+            logits = torch.empty(S, self.V_local, dtype=self.dtype, device=x.device)
+        else:
+            xs = self.ws_logits_x[:S]
+            logits = self.ws_logits[:S]
         torch.index_select(x, 0, idx, out=xs)
-        logits = self.ws_logits[:S]
         if S <= L.SKINNY_MAX and x.is_cuda:
             L.gemm_skinny_bf16(xs, self.lm_head, out=logits)
         else:

@@ -75,7 +75,9 @@ class ModelRunner:
         self.graphs: dict[int, tuple] = {}
         self.seed = seed
         self.num_sms = torch.cuda.get_device_properties(self.device).multi_processor_count if self.is_cuda else 148
-        max_layout = Layout(self.max_tokens, max_num_seqs, max_num_seqs, self._max_work(), self.max_blocks)
+        # logits rows: one per sampling request, or 1 + drafts for verified requests (<= tokens)
+        max_layout = Layout(self.max_tokens, max_num_seqs, max(max_num_seqs, self.max_tokens), self._max_work(),
+                            self.max_blocks)
         pin = self.is_cuda
         # Two pinned input buffers and two pinned output buffers: with asynchronous
         # scheduling, step N+1 is packed while step N's copies may still be in flight.
@@ -165,7 +167,11 @@ class ModelRunner:
             st = sr.start
             P = req.num_prompt_tokens
             known = P + len(req.output_token_ids)
-            if st + n > known:
+            if sr.spec:
+                # the last known token, then the drafts being verified
+                ids[t] = req.token_at(st)
+                ids[t + 1:t + n] = sr.spec
+            elif st + n > known:
                 # the last input token was sampled by a step still in flight: it is read on
                 # the device from the request's slot (id = -(slot + 1))
                 nk = max(0, known - st)
@@ -190,8 +196,9 @@ class ModelRunner:
             bt[i, :nb] = blocks
             bt[i, nb:] = 0
             t += n
-            if sr.samples:
-                lidx[s] = t - 1
+            nl = sr.num_logits
+            for j in range(nl):
+                lidx[s] = t - nl + j
                 sp = req.sampling_params
                 temp[s] = 0.0 if sp.greedy else sp.temperature
                 topk[s] = sp.top_k or 0
@@ -318,7 +325,7 @@ class ModelRunner:
             return StepHandle(None, None, None, 0)
         if out.num_tokens > self.max_tokens:
             raise ValueError(f"batch of {out.num_tokens} tokens exceeds max_num_batched_tokens")
-        S = sum(1 for s in out.scheduled if s.samples)
+        S = sum(s.num_logits for s in out.scheduled)
         self._buf_idx ^= 1
         self.host_buf = self.host_bufs[self._buf_idx]
         self.host_np = self.host_buf.numpy()
@@ -375,7 +382,7 @@ class ModelRunner:
         """Run one step eagerly and return the full-vocabulary logits of its sampling rows
         (``[S, V]``, model dtype) instead of sampling (logit validation / accuracy tooling)."""
         B = len(out.scheduled)
-        S = sum(1 for s in out.scheduled if s.samples)
+        S = sum(s.num_logits for s in out.scheduled)
         self._buf_idx ^= 1
         self.host_buf = self.host_bufs[self._buf_idx]
         self.host_np = self.host_buf.numpy()
