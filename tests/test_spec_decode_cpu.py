@@ -60,3 +60,34 @@ def test_ngram_spec_decode_matches_greedy():
     assert [o.outputs[0].token_ids for o in got] == [o.outputs[0].token_ids for o in ref]
     m = llm.engine.metrics
     assert m.spec_draft_tokens > 0
+
+
+def test_eagle3_spec_decode_matches_greedy(tmp_path):
+    """An EAGLE3 draft head (random weights, saved in the checkpoint layout and loaded back)
+    proposes; output must equal plain greedy decoding."""
+    from safetensors.torch import save_file
+
+    d, _ = tiny_llama_checkpoint()
+    H, Hq, Hkv, D, I, V = 256, 4, 2, 64, 512, 32000
+    g = torch.Generator().manual_seed(3)
+    r = lambda *s: torch.randn(*s, generator=g) * 0.05  # noqa: E731
+    t = {"fc.weight": r(H, 3 * H), "norm.weight": torch.ones(H), "lm_head.weight": r(V, H),
+         "d2t": torch.zeros(V, dtype=torch.int64)}
+    for n, shape in (("self_attn.q_proj.weight", (Hq * D, 2 * H)), ("self_attn.k_proj.weight", (Hkv * D, 2 * H)),
+                     ("self_attn.v_proj.weight", (Hkv * D, 2 * H)), ("self_attn.o_proj.weight", (H, Hq * D)),
+                     ("mlp.gate_proj.weight", (I, H)), ("mlp.up_proj.weight", (I, H)), ("mlp.down_proj.weight", (H, I))):
+        t["midlayer." + n] = r(*shape)
+    for n in ("input_layernorm", "hidden_norm", "post_attention_layernorm"):
+        t[f"midlayer.{n}.weight"] = torch.ones(H)
+    save_file(t, str(tmp_path / "model.safetensors"))
+    (tmp_path / "config.json").write_text('{"architectures": ["LlamaForCausalLMEagle3"], "intermediate_size": 512}')
+    prompts = random_prompts(n=2, length=20)
+    sp = SamplingParams(temperature=0, max_tokens=12, ignore_eos=True)
+    kw = dict(device="cpu", dtype="float32", max_num_seqs=4, max_model_len=256, num_gpu_blocks=64,
+              max_num_batched_tokens=64)
+    ref = LLM(d, **kw).generate(prompts, sp)
+    llm = LLM(d, speculative_config={"method": "eagle3", "num_speculative_tokens": 3, "model": str(tmp_path),
+                                     "aux_layers": [0, 1, 1]}, **kw)
+    got = llm.generate(prompts, sp)
+    assert [o.outputs[0].token_ids for o in got] == [o.outputs[0].token_ids for o in ref]
+    assert llm.engine.metrics.spec_draft_tokens > 0

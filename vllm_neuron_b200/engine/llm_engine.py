@@ -247,8 +247,6 @@ class LLMEngine:
         self.num_steps += 1
         self.metrics.steps += 1
         logits = self.runner.forward_logits(out)
-        if hasattr(self.proposer, "observe"):
-            self.proposer.observe(out)
         samplers = [s for s in out.scheduled if s.samples]
         drafts = [list(s.spec) for s in samplers]
         temps = [0.0 if s.req.sampling_params.greedy else s.req.sampling_params.temperature for s in samplers]
@@ -262,10 +260,14 @@ class LLMEngine:
                                * 1000003 + len(s.req.output_token_ids)) & 0x7FFFFFFFFFFFFFFF)
             gens.append(g)
         toks = rejection_sample(logits, drafts, temps, gens)
+        if hasattr(self.proposer, "observe"):
+            self.proposer.observe(out, toks)
         self.metrics.spec_draft_tokens += sum(len(d) for d in drafts)
         self.metrics.spec_accepted_tokens += sum(len(t) - 1 for t, d in zip(toks, drafts) if d)
         finished = self.scheduler.update_spec(out, toks, now=time.perf_counter())
         for req in finished:
+            if hasattr(self.proposer, "release"):
+                self.proposer.release(req.request_id)
             if req.slot >= 0:
                 self._free_slots.append(req.slot)
                 req.slot = -1

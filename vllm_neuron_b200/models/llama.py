@@ -108,6 +108,9 @@ class LlamaForCausalLM(torch.nn.Module):
         self.kv_caches: list[tuple[torch.Tensor, torch.Tensor]] = []
         self._alloc_workspace(max_tokens, max_decode_tokens, max_seqs)
         self.tp_fused = None  # TPFusedComm: fused all-reduce + residual + RMSNorm (decode)
+        # Hidden states captured after these layers (EAGLE3 drafting): [tokens, len * H]
+        self.aux_layers: list[int] = []
+        self.aux_hidden: torch.Tensor | None = None
 
     # ---------------------------------------------------------------- init / weights
     def _make_attn(self, m, p, layer: int):
@@ -239,7 +242,16 @@ class LlamaForCausalLM(torch.nn.Module):
             # ---- MLP
             nxt_norm = self.layers[i + 1].input_norm if i + 1 < nL else self.final_norm
             self._mlp(i, ly, x, res, nxt_norm, T, small, fused)
+            if self.aux_layers and i in self.aux_layers:
+                j = self.aux_layers.index(i)
+                self.aux_hidden[:T, j * self.H:(j + 1) * self.H].copy_(res)
         return self.compute_logits(x, b.logits_indices)
+
+    def enable_aux_hidden(self, layers: list[int]):
+        """Capture the residual stream after ``layers`` in every forward (draft models)."""
+        self.aux_layers = list(layers)
+        self.aux_hidden = torch.zeros(self.max_tokens, len(layers) * self.H, dtype=self.dtype,
+                                      device=self.device)
 
     def _mlp(self, i: int, ly, x, res, nxt_norm, T: int, small: bool, fused: bool):
         """Dense SwiGLU MLP; leaves ``x = nxt_norm(res += mlp(x))``."""
