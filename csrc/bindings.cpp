@@ -566,6 +566,19 @@ void sigmoid_gate_mul(at::Tensor& x, const at::Tensor& gate) {
   check_launch("sigmoid_gate_mul", x.size(0) > 0 ? 1 : 0);
 }
 
+void apply_token_bitmask(at::Tensor& logits, const at::Tensor& mask) {
+  CHECK_CUDA(logits);
+  CHECK_BF16(logits);
+  TORCH_CHECK(mask.scalar_type() == at::kInt && mask.is_contiguous() && mask.size(0) == logits.size(0),
+              "bitmask must be int32 [rows, ceil(V / 32)]");
+  TORCH_CHECK(logits.stride(1) == 1 && mask.size(1) * 32 >= logits.size(1), "apply_token_bitmask: shapes");
+  const c10::cuda::CUDAGuard guard(logits.device());
+  b200::apply_token_bitmask_launch(reinterpret_cast<__nv_bfloat16*>(logits.data_ptr()), logits.stride(0),
+                                   (int)logits.size(0), (int)logits.size(1), mask.data_ptr<int32_t>(),
+                                   (int)mask.size(1), cur_stream());
+  check_launch("apply_token_bitmask", logits.size(0) > 0 ? 1 : 0);
+}
+
 int64_t num_sms() { return b200::num_sms_cached(); }
 int64_t launch_count() { return g_launches.load(); }
 
@@ -600,4 +613,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("causal_conv1d", &causal_conv1d);
   m.def("gated_delta_rule", &gated_delta_rule);
   m.def("sigmoid_gate_mul", &sigmoid_gate_mul);
+  m.def("apply_token_bitmask", &apply_token_bitmask);
 }

@@ -61,6 +61,9 @@ struct SampleParams {
 };
 void sample_launch(const SampleParams& p, cudaStream_t stream);
 
+void apply_token_bitmask_launch(__nv_bfloat16* logits, long long stride, int rows, int V,
+                                const int32_t* mask, int words, cudaStream_t stream);
+
 void argmax_launch(const void* logits, bool f32, long long stride, int B, int V, int* out_idx,
                    float* out_val, int vocab_offset, cudaStream_t stream);
 

@@ -309,4 +309,26 @@ void argmax_launch(const void* logits, bool f32, long long stride, int B, int V,
              out_val, vocab_offset);
 }
 
+// Structured outputs: logits[r, i] = -inf where bit i of row r's token bitmask is 0
+// (bitmask int32 [rows, ceil(V / 32)], bit i % 32 of word i / 32; reference:
+// vllm_neuron/vllm/core/scheduler.py:940-952 attaches the grammar bitmask, applied before
+// sampling in nn/sampler.py:13-169).
+__global__ void apply_token_bitmask_kernel(__nv_bfloat16* logits, long long stride, int V,
+                                           const int32_t* __restrict__ mask, int words) {
+  pdl_trigger();
+  pdl_wait();
+  const int r = blockIdx.y;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= V) return;
+  const uint32_t w = (uint32_t)mask[(long long)r * words + (i >> 5)];
+  if (!((w >> (i & 31)) & 1u)) logits[(long long)r * stride + i] = __float2bfloat16(-INFINITY);
+}
+
+void apply_token_bitmask_launch(__nv_bfloat16* logits, long long stride, int rows, int V,
+                                const int32_t* mask, int words, cudaStream_t stream) {
+  if (rows == 0) return;
+  launch_pdl(apply_token_bitmask_kernel, dim3((V + 255) / 256, rows), dim3(256), 0, stream, logits,
+             stride, V, mask, words);
+}
+
 }  // namespace b200

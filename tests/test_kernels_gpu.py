@@ -281,3 +281,15 @@ def test_device_resident_tokens(cuda_device):
     ids = torch.tensor([-(5 + 1), 17, -(7 + 1)], dtype=torch.int32, device=cuda_device)
     out = ops.embedding(ids, table, last_tok=last)
     assert torch.equal(out[0], table[tok[0]]) and torch.equal(out[1], table[17]) and torch.equal(out[2], table[tok[2]])
+
+
+def test_apply_token_bitmask(cuda_device):
+    from vllm_neuron_b200.ops.sampling import apply_token_bitmask
+
+    V = 1000
+    logits = torch.randn(5, V, device=cuda_device).to(torch.bfloat16)
+    mask = torch.randint(-2**31, 2**31 - 1, (5, (V + 31) // 32), dtype=torch.int32)
+    ref = logits.cpu().float().clone()
+    apply_token_bitmask(ref, mask)
+    apply_token_bitmask(logits, mask.to(cuda_device))
+    assert torch.equal(torch.isinf(logits.cpu().float()), torch.isinf(ref))

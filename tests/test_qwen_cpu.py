@@ -70,3 +70,23 @@ def test_qwen2_moe_shared_expert():
                          max_position_embeddings=256, initializer_range=0.05, qkv_bias=True)
     hf = Qwen2MoeForCausalLM(cfg).float().eval()
     _check(_save(hf), hf, 512)
+
+
+def test_qwen3_embedding_pooling():
+    """Qwen3-Embedding style: encoder-only Qwen3Model checkpoint, LAST-token pooling, L2 norm."""
+    from transformers import Qwen3Config, Qwen3Model
+
+    torch.manual_seed(3)
+    cfg = Qwen3Config(hidden_size=64, num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
+                      head_dim=16, intermediate_size=128, vocab_size=512, max_position_embeddings=256,
+                      initializer_range=0.05)
+    hf = Qwen3Model(cfg).float().eval()
+    d = _save(hf)
+    prompts = random_prompts(n=3, length=17, vocab=512)
+    llm = LLM(d, device="cpu", dtype="float32", max_num_seqs=4, max_model_len=128, num_gpu_blocks=64,
+              max_num_batched_tokens=128)
+    got = torch.tensor([o.embedding for o in llm.embed(prompts)])
+    with torch.no_grad():
+        ref = torch.stack([hf(torch.tensor([p])).last_hidden_state[0, -1] for p in prompts])
+    ref = torch.nn.functional.normalize(ref, dim=-1)
+    assert torch.allclose(got, ref, atol=2e-3)  # the QK-norm output is rounded to bf16 as on the GPU

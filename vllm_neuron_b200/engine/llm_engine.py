@@ -129,6 +129,10 @@ class LLMEngine:
                                  else bool(args.async_scheduling))
         self._inflight = None  # (SchedulerOutput, StepHandle) of the launched, unprocessed step
         self._free_slots = list(range(self.runner.max_slots - 2, -1, -1))
+        self.tokenizer = None          # set by the LLM front end when it loads one
+        self.structured_vocab = None   # token strings, for grammars on token-id-only engines
+        self._structured = None
+        self._has_structured = False
         self.proposer = None
         if args.speculative_config:
             self.proposer = self._make_proposer(dict(args.speculative_config))
@@ -140,6 +144,9 @@ class LLMEngine:
         params = SamplingParams.coerce(params)
         rid = request_id if request_id is not None else str(next(self._ids))
         req = Request(rid, list(prompt_token_ids), params, eos_token_id=self.eos_token_id)
+        if params.structured_outputs:
+            req.matcher = self.structured_outputs().matcher(params.structured_outputs)
+            self._has_structured = True
         if arrival_time is not None:
             req.arrival_time = arrival_time
         if not self._free_slots:
@@ -169,7 +176,13 @@ class LLMEngine:
                                "(a peer rank stopped or fell out of step)")
 
     @torch.no_grad()
-    def prompt_logits(self, prompts: list[list[int]]) -> torch.Tensor:
+    def prompt_hidden(self, prompts: list[list[int]]) -> torch.Tensor:
+        """Final-norm hidden state of the last prompt position of each prompt ``[N, H]`` fp32
+        (pooling / embedding models)."""
+        return self.prompt_logits(prompts, hidden=True)
+
+    @torch.no_grad()
+    def prompt_logits(self, prompts: list[list[int]], hidden: bool = False) -> torch.Tensor:
         """Logits of the last prompt position of each prompt (one prefill step, nothing is
         sampled or kept): the hook of the logit-validation tooling.  Returns ``[N, V]`` fp32 on
         the CPU.  Must be called with no requests in flight."""
@@ -187,7 +200,7 @@ class LLMEngine:
                 reqs.append(r)
             out = SchedulerOutput([ScheduledRequest(r, 0, r.num_prompt_tokens, True) for r in reqs],
                                   sum(r.num_prompt_tokens for r in reqs))
-            return self.runner.forward_logits(out).float().cpu()
+            return self.runner.forward_logits(out, hidden=hidden).float().cpu()
         finally:
             for r in reqs:
                 self.block_manager.free_request(r)
@@ -213,6 +226,52 @@ class LLMEngine:
             if r.status.finished and r.num_pending == 0 and r.slot >= 0:
                 self._free_slots.append(r.slot)
                 r.slot = -1
+        return finished
+
+    # ---------------------------------------------------------------- structured outputs
+    def structured_outputs(self):
+        """The grammar manager (created on first use from the tokenizer, or from
+        ``self.structured_vocab`` when the engine runs on token ids only)."""
+        if self._structured is None:
+            from .structured import StructuredOutputManager
+
+            eos = [self.eos_token_id] if self.eos_token_id is not None else None
+            self._structured = StructuredOutputManager(self.arch.vocab_size, tokenizer=self.tokenizer,
+                                                       vocab=self.structured_vocab, stop_token_ids=eos)
+        return self._structured
+
+    def _structured_step(self) -> list[Request]:
+        """Synchronous step with grammar bitmasks for the requests that have one."""
+        finished = []
+        if self._inflight is not None:
+            finished += self._process(*self._inflight)
+            self._inflight = None
+        out = self.scheduler.schedule()
+        if out.empty:
+            return finished
+        samplers = [s.req for s in out.scheduled if s.samples]
+        mask = self.structured_outputs().bitmask([getattr(r, "matcher", None) for r in samplers])
+        before = {r.request_id: len(r.output_token_ids) for r in samplers}
+        want_lp = any(r.sampling_params.logprobs for r in samplers)
+        handle = self.runner.launch(out, want_logprobs=want_lp, bitmask=mask)
+        self.num_steps += 1
+        self.metrics.steps += 1
+        finished += self._process(out, handle)
+        now = time.perf_counter()
+        for r in samplers:
+            m = getattr(r, "matcher", None)
+            if m is None or len(r.output_token_ids) == before[r.request_id]:
+                continue
+            for tok in r.output_token_ids[before[r.request_id]:]:
+                if not m.is_terminated():
+                    m.accept_token(int(tok))
+            if m.is_terminated() and not r.status.finished:
+                self.scheduler.finish_request(r, RequestStatus.FINISHED_STOPPED, now)
+                r.stop_reason = "grammar"
+                finished.append(r)
+                if r.slot >= 0 and r.num_pending == 0:
+                    self._free_slots.append(r.slot)
+                    r.slot = -1
         return finished
 
     # ---------------------------------------------------------------- speculative decoding
@@ -278,6 +337,9 @@ class LLMEngine:
         previous step are processed while this one runs on the GPU."""
         if self.proposer is not None:
             return self._spec_step()
+        if self._has_structured and any(getattr(r, "matcher", None) is not None
+                                        for r in self.scheduler.requests.values()):
+            return self._structured_step()
         out = self.scheduler.schedule()
         handle = None
         if not out.empty:

@@ -18,6 +18,8 @@ class SamplingParams:
     stop_token_ids: list[int] = field(default_factory=list)
     logprobs: int | None = None
     detokenize: bool = True
+    # {"json": schema} | {"json_object": True} | {"regex": r} | {"choice": [..]} | {"grammar": ebnf}
+    structured_outputs: dict | None = None
 
     @classmethod
     def coerce(cls, sp) -> "SamplingParams":
@@ -27,7 +29,7 @@ class SamplingParams:
             return sp
         out = cls()
         for name in ("n", "temperature", "top_p", "top_k", "min_p", "seed", "max_tokens",
-                     "min_tokens", "ignore_eos", "logprobs", "detokenize"):
+                     "min_tokens", "ignore_eos", "logprobs", "detokenize", "structured_outputs"):
             if hasattr(sp, name):
                 setattr(out, name, getattr(sp, name))
         stop = getattr(sp, "stop_token_ids", None) or []

@@ -100,6 +100,15 @@ class Scheduler:
         self.bm.free_request(req)
         req.status = RequestStatus.FINISHED_ABORTED
 
+    def finish_request(self, req: Request, status: RequestStatus, now: float | None = None):
+        """Finish a running request outside the token stop checks (e.g. a completed grammar)."""
+        req.status = status
+        req.finish_time = now
+        if req in self.running:
+            self.running.remove(req)
+        self.bm.free_request(req)
+        self.requests.pop(req.request_id, None)
+
     def has_unfinished(self) -> bool:
         return bool(self.waiting or self.running)
 

@@ -18,6 +18,13 @@ from ..engine.sampling_params import SamplingParams
 from ..parallel import state as ps
 
 
+class EmbeddingOutput:
+    def __init__(self, prompt_token_ids: list[int], embedding: list[float]):
+        self.prompt_token_ids = prompt_token_ids
+        self.outputs = type("Pooled", (), {"embedding": embedding, "data": embedding})()
+        self.embedding = embedding
+
+
 def _normalize_prompt(p: Any, tokenizer) -> list[int]:
     if isinstance(p, dict):
         if "prompt_token_ids" in p:
@@ -72,6 +79,7 @@ class LLM:
                 from transformers import AutoTokenizer
 
                 self.tokenizer = AutoTokenizer.from_pretrained(path)
+        self.engine.tokenizer = self.tokenizer
 
     def get_tokenizer(self):
         return self.tokenizer
@@ -97,6 +105,24 @@ class LLM:
                     c.text = self.tokenizer.decode(c.token_ids, skip_special_tokens=True)
             outs.append(o)
         return outs
+
+    def embed(self, prompts, normalize: bool = True, batch_size: int | None = None) -> list["EmbeddingOutput"]:
+        """Pooling API (embedding models such as Qwen3-Embedding): last-token pooling of the
+        final hidden state, L2-normalised (reference: the runner's ``_pool``, LAST + normalize,
+        vllm_neuron/vllm/worker/neuron_model_runner.py:7984 and model/pooling_adapter.py)."""
+        if isinstance(prompts, (str, dict)) or (isinstance(prompts, list) and prompts and isinstance(prompts[0], int)):
+            prompts = [prompts]
+        toks = [_normalize_prompt(p, self.tokenizer) for p in prompts]
+        bs = batch_size or self.engine.args.max_num_seqs
+        outs = []
+        for i in range(0, len(toks), bs):
+            h = self.engine.prompt_hidden(toks[i:i + bs])
+            if normalize:
+                h = torch.nn.functional.normalize(h, dim=-1)
+            outs += [EmbeddingOutput(t, e.tolist()) for t, e in zip(toks[i:i + bs], h)]
+        return outs
+
+    encode = embed
 
     def shutdown(self):
         self.engine.shutdown()

@@ -53,6 +53,7 @@ class ForwardBatch:
     num_tokens: int
     last_tok: torch.Tensor | None = None  # device-resident tokens for ids < 0
     seq_slots: torch.Tensor | None = None  # [B] int32 per-request state-cache slots
+    want_hidden: bool = False  # return the final-norm hidden states of the logits rows (pooling)
 
 
 def _shard(n: int, world: int, rank: int) -> tuple[int, int]:
@@ -245,6 +246,8 @@ class LlamaForCausalLM(torch.nn.Module):
             if self.aux_layers and i in self.aux_layers:
                 j = self.aux_layers.index(i)
                 self.aux_hidden[:T, j * self.H:(j + 1) * self.H].copy_(res)
+        if b.want_hidden:
+            return x.index_select(0, b.logits_indices.long())
         return self.compute_logits(x, b.logits_indices)
 
     def enable_aux_hidden(self, layers: list[int]):

@@ -150,6 +150,8 @@ class Qwen3_5MoeForCausalLM(Qwen3MoeForCausalLM):
             ops.add_rmsnorm(h, res, ly.post_norm, self.eps, out=x)
             nxt_norm = self.layers[i + 1].input_norm if i + 1 < nL else self.final_norm
             self._moe_mlp(ly, x, res, nxt_norm, T)
+        if b.want_hidden:
+            return x.index_select(0, b.logits_indices.long())
         return self.compute_logits(x, b.logits_indices)
 
 

@@ -8,6 +8,9 @@ _MODELS = {
     "MistralForCausalLM": ("vllm_neuron_b200.models.llama", "LlamaForCausalLM"),
     "Qwen3ForCausalLM": ("vllm_neuron_b200.models.llama", "LlamaForCausalLM"),
     "Qwen2ForCausalLM": ("vllm_neuron_b200.models.llama", "LlamaForCausalLM"),
+    # embedding backbones (pooling through LLM.embed)
+    "Qwen3Model": ("vllm_neuron_b200.models.llama", "LlamaForCausalLM"),
+    "LlamaModel": ("vllm_neuron_b200.models.llama", "LlamaForCausalLM"),
     "GptOssForCausalLM": ("vllm_neuron_b200.models.gpt_oss", "GptOssForCausalLM"),
     "Qwen3MoeForCausalLM": ("vllm_neuron_b200.models.qwen_moe", "Qwen3MoeForCausalLM"),
     "Qwen2MoeForCausalLM": ("vllm_neuron_b200.models.qwen_moe", "Qwen2MoeForCausalLM"),

@@ -84,3 +84,14 @@ def sample_ref(logits, temperature, top_k, top_p, seeds, offsets, min_p=None) ->
         g = torch.Generator().manual_seed(int(seeds[b]) * 1000003 + int(offsets[b]))
         out[b] = int(torch.multinomial(probs, 1, generator=g))
     return out.to(logits.device)
+
+
+def apply_token_bitmask(logits: torch.Tensor, mask: torch.Tensor) -> torch.Tensor:
+    """``logits[r, i] = -inf`` where bit ``i`` of ``mask[r]`` (int32 words) is 0."""
+    if not logits.is_cuda:
+        V = logits.shape[1]
+        bits = ((mask.to(torch.int64)[:, :, None] >> torch.arange(32)) & 1).reshape(mask.shape[0], -1)[:, :V]
+        logits.masked_fill_(bits.to(logits.device) == 0, float("-inf"))
+        return logits
+    ext().apply_token_bitmask(logits, mask)
+    return logits

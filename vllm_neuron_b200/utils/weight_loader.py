@@ -93,7 +93,10 @@ def load_dense_decoder(model, get_tensor: Callable[[str], torch.Tensor], names: 
     _copy(model.final_norm, get_tensor(pre + "norm.weight"), "norm")
     if not cfg.tie_word_embeddings:
         head = "lm_head.weight"
-        _copy(model.lm_head, shard_rows(get_tensor(head), W, r, model.V_local), "lm_head")
+        if head in names:
+            _copy(model.lm_head, shard_rows(get_tensor(head), W, r, model.V_local), "lm_head")
+        else:  # encoder-only checkpoints (embedding models) carry no LM head
+            model.lm_head = model.embed
 
 
 def _expert_tensor(get_tensor, names, base: str) -> torch.Tensor:

@@ -264,8 +264,10 @@ class ModelRunner:
         return fb, samp
 
     def _forward_and_sample(self, fb: ForwardBatch, samp: dict, S: int, tok_out: torch.Tensor,
-                            lp_out: torch.Tensor | None):
+                            lp_out: torch.Tensor | None, bitmask: torch.Tensor | None = None):
         logits = self.model.forward(fb)
+        if bitmask is not None:
+            ops.sampling.apply_token_bitmask(logits, bitmask)
         ops.sample(logits, samp["temperature"], samp["top_k"], samp["top_p"], samp["seeds"],
                    samp["offsets"], min_p=samp["min_p"], out=tok_out[:S],
                    out_logprob=lp_out[:S] if lp_out is not None else None,
@@ -318,7 +320,8 @@ class ModelRunner:
         self.graphs.clear()
 
     # ------------------------------------------------------------------ execute
-    def launch(self, out: SchedulerOutput, want_logprobs: bool = False) -> "StepHandle":
+    def launch(self, out: SchedulerOutput, want_logprobs: bool = False,
+               bitmask: torch.Tensor | None = None) -> "StepHandle":
         """Enqueue one step (inputs H2D, forward, sampling, tokens D2H) without waiting."""
         B = len(out.scheduled)
         if B == 0:
@@ -331,7 +334,7 @@ class ModelRunner:
         self.host_np = self.host_buf.numpy()
         tok_host, lp_host = self.tok_hosts[self._buf_idx], self.lp_hosts[self._buf_idx]
         bucket = None
-        if self.use_graphs and out.is_pure_decode and self.graphs:
+        if self.use_graphs and out.is_pure_decode and self.graphs and bitmask is None:
             for bb in sorted(self.graphs):
                 if bb >= B:
                     bucket = bb
@@ -357,7 +360,8 @@ class ModelRunner:
             fb, samp = self._views(dev, lay, B, S, W, decode, splits)
             fb.work = fb.work[:W]
             if S > 0:
-                self._forward_and_sample(fb, samp, S, self.tok_dev, self.lp_dev)
+                mask = bitmask.to(self.device, non_blocking=True) if bitmask is not None else None
+                self._forward_and_sample(fb, samp, S, self.tok_dev, self.lp_dev, mask)
             else:
                 self.model.forward(fb)
             self.num_eager_steps += 1
@@ -378,7 +382,7 @@ class ModelRunner:
         return StepHandle(ev, tok_host, lps, S)
 
     @torch.no_grad()
-    def forward_logits(self, out: SchedulerOutput) -> torch.Tensor:
+    def forward_logits(self, out: SchedulerOutput, hidden: bool = False) -> torch.Tensor:
         """Run one step eagerly and return the full-vocabulary logits of its sampling rows
         (``[S, V]``, model dtype) instead of sampling (logit validation / accuracy tooling)."""
         B = len(out.scheduled)
@@ -393,6 +397,7 @@ class ModelRunner:
         dev.copy_(self.host_buf[:lay.total], non_blocking=self.is_cuda)
         fb, _ = self._views(dev, lay, B, S, W, decode, splits)
         fb.work = fb.work[:W]
+        fb.want_hidden = hidden
         logits = self.model.forward(fb).clone()
         if self.is_cuda:
             torch.cuda.synchronize(self.device)
