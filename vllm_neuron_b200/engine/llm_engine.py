@@ -228,6 +228,37 @@ class LLMEngine:
                 r.slot = -1
         return finished
 
+    # ---------------------------------------------------------------- profiling
+    def start_profile(self, out_dir: str | None = None):
+        """Start a device + host profile (torch.profiler with CUDA activities); ``stop_profile``
+        writes a Chrome trace under ``out_dir`` (env ``VLLM_B200_PROFILE_DIR`` by default).
+        Counterpart of the reference's /start_profile hook (NeuronProfiler,
+        vllm_neuron/vllm/worker/neuron_profiler.py:38-110)."""
+        import os
+
+        from torch.profiler import ProfilerActivity, profile
+
+        self._profile_dir = out_dir or os.environ.get("VLLM_B200_PROFILE_DIR", "b200_profile")
+        acts = [ProfilerActivity.CPU] + ([ProfilerActivity.CUDA] if self.device.type == "cuda" else [])
+        self._profiler = profile(activities=acts, record_shapes=False)
+        self._profiler.__enter__()
+
+    def stop_profile(self) -> str | None:
+        import os
+
+        prof = getattr(self, "_profiler", None)
+        if prof is None:
+            return None
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+        prof.__exit__(None, None, None)
+        os.makedirs(self._profile_dir, exist_ok=True)
+        rank = self.tp.rank
+        path = os.path.join(self._profile_dir, f"trace_rank{rank}_{int(time.time())}.json")
+        prof.export_chrome_trace(path)
+        self._profiler = None
+        return path
+
     # ---------------------------------------------------------------- structured outputs
     def structured_outputs(self):
         """The grammar manager (created on first use from the tokenizer, or from

@@ -102,6 +102,13 @@ class ModelRunner:
         self.graph_kernels: dict[int, int] = {}  # kernels recorded per captured bucket
         self.replayed_kernels = 0
         self.kv_cache = None
+        # Snapshot capture: when set, the packed inputs of every step are saved to this
+        # directory (reference: vllm_neuron/snapshot/*, runtime input capture).
+        import os
+
+        self.snapshot_dir = os.environ.get("VLLM_B200_SNAPSHOT_DIR") or None
+        self.snapshot_max = int(os.environ.get("VLLM_B200_SNAPSHOT_MAX_STEPS", "64"))
+        self._snap_n = 0
 
     def _max_work(self) -> int:
         # prefill work items: ceil(q_len * G / 64) per sequence, bounded by tokens*G/64 + seqs
@@ -241,6 +248,21 @@ class ModelRunner:
         self._last_work_len = len(w.work)
         return s, w.decode, w.num_splits
 
+    def _snapshot(self, out: SchedulerOutput, lay: Layout, decode: bool, splits: int):
+        """Save one step's device inputs (the packed int32 buffer and its layout)."""
+        import os
+
+        if self._snap_n >= self.snapshot_max:
+            return
+        os.makedirs(self.snapshot_dir, exist_ok=True)
+        torch.save({"step": self._snap_n, "layout": dict(T=lay.T, B=lay.B, S=lay.S, W=lay.W, nblk=lay.nblk),
+                    "offsets": lay.off, "buffer": self.host_buf[:lay.total].clone(), "decode": decode,
+                    "num_splits": splits, "work_len": getattr(self, "_last_work_len", 0),
+                    "requests": [(s.req.request_id, s.start, s.num_tokens, s.samples, list(s.spec))
+                                 for s in out.scheduled]},
+                   os.path.join(self.snapshot_dir, f"step_{self._snap_n:06d}.pt"))
+        self._snap_n += 1
+
     def _views(self, buf: torch.Tensor, lay: Layout, B: int, S: int, W: int, decode: bool, splits: int) -> tuple:
         o = lay.off
 
@@ -342,6 +364,8 @@ class ModelRunner:
         if bucket is not None:
             g, lay, buf, tok, lp, splits = self.graphs[bucket]
             self._pack(out, lay, pad_B=bucket)
+            if self.snapshot_dir:
+                self._snapshot(out, lay, True, splits)
             n = lay.total
             buf.copy_(self.host_buf[:n], non_blocking=True)
             self.h2d_bytes += n * 4
@@ -353,6 +377,8 @@ class ModelRunner:
             lay = Layout(out.num_tokens, B, S, self._max_work_for(out), self.max_blocks)
             S2, decode, splits = self._pack(out, lay)
             W = self._last_work_len
+            if self.snapshot_dir:
+                self._snapshot(out, lay, decode, splits)
             n = lay.total
             dev = self.dev_buf[:n]
             dev.copy_(self.host_buf[:n], non_blocking=self.is_cuda)
