@@ -16,7 +16,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, ckpt, prompts, q):
+def _worker(rank, world, port, ckpt, prompts, q, tp=None):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
                       WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
     import torch
@@ -27,7 +27,7 @@ def _worker(rank, world, port, ckpt, prompts, q):
     from vllm_neuron_b200.parallel import state as ps
 
     try:
-        llm = LLM(ckpt, tensor_parallel_size=world, device="cpu", max_num_seqs=8, max_model_len=128,
+        llm = LLM(ckpt, tensor_parallel_size=tp or world, device="cpu", max_num_seqs=8, max_model_len=128,
                   num_gpu_blocks=64, max_num_batched_tokens=48)
         outs = llm.generate(prompts, SamplingParams(temperature=0, max_tokens=8, ignore_eos=True))
         q.put((rank, [o.outputs[0].token_ids for o in outs]))
@@ -50,6 +50,29 @@ def test_tp2_matches_tp1():
     q = ctx.Queue()
     port = _free_port()
     procs = [ctx.Process(target=_worker, args=(r, 2, port, ckpt, prompts, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert res[0] == ref, res[0]
+    assert res[1] == ref, res[1]
+
+
+def test_dp2_matches_single_replica():
+    """Two data-parallel replicas (TP=1 each) split the requests and gather the outputs."""
+    ckpt, _ = tiny_llama_checkpoint()
+    prompts = random_prompts(n=5, length=16, seed=12)
+    from vllm_neuron_b200.engine.sampling_params import SamplingParams
+    from vllm_neuron_b200.entrypoints import LLM
+
+    ref = LLM(ckpt, device="cpu", max_num_seqs=8, max_model_len=128, num_gpu_blocks=64,
+              max_num_batched_tokens=48).generate(prompts, SamplingParams(temperature=0, max_tokens=8, ignore_eos=True))
+    ref = [o.outputs[0].token_ids for o in ref]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, ckpt, prompts, q, 1)) for r in range(2)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=300) for _ in procs)

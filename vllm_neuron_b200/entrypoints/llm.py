@@ -51,15 +51,26 @@ class LLM:
                  skip_tokenizer_init: bool = False, num_gpu_blocks: int | None = None,
                  enforce_eager: bool = False, device: str | None = None, dtype: str = "auto",
                  async_scheduling: bool | None = None, speculative_config: dict | None = None,
-                 **unused):
+                 data_parallel_size: int | None = None, **unused):
         if device is None:
             device = f"cuda:{torch.cuda.current_device()}" if torch.cuda.is_available() else "cpu"
         ps.init_distributed(backend="gloo" if str(device).startswith("cpu") else None)
         world = torch.distributed.get_world_size() if torch.distributed.is_initialized() else 1
-        if tensor_parallel_size != world and world > 1:
-            raise ValueError(f"tensor_parallel_size={tensor_parallel_size} but {world} ranks were launched")
+        if world % tensor_parallel_size:
+            raise ValueError(f"tensor_parallel_size={tensor_parallel_size} does not divide the {world} launched ranks")
+        dp = world // tensor_parallel_size
+        if data_parallel_size not in (None, dp):
+            raise ValueError(f"data_parallel_size={data_parallel_size} but TP={tensor_parallel_size} x "
+                             f"{world} ranks give {dp}")
         st = ps.initialize_parallel_state(ps.ParallelConfig(world_size=world,
-                                                            tensor_parallel_size=tensor_parallel_size))
+                                                            tensor_parallel_size=tensor_parallel_size,
+                                                            data_parallel_size=dp))
+        # Data parallelism: each group of TP ranks is an independent engine replica serving
+        # every dp-th request; outputs are gathered over the DP group (reference: data
+        # parallel replicas, docs/design/parallelism/data_parallelism.md).
+        self.dp_size = dp
+        self.dp_rank = (torch.distributed.get_rank() // tensor_parallel_size) if world > 1 else 0
+        self._dp_group = st.dp_cpu
         if dtype == "auto":
             dtype = "bfloat16" if str(device).startswith("cuda") else "float32"
         args = EngineArgs(model=model, max_num_seqs=max_num_seqs,
@@ -91,6 +102,22 @@ class LLM:
         prompts = list(prompts)
         if not isinstance(sampling_params, list):
             sampling_params = [sampling_params] * len(prompts)
+        if self.dp_size > 1:
+            return self._generate_dp(prompts, sampling_params)
+        return self._generate(prompts, sampling_params)
+
+    def _generate_dp(self, prompts, sampling_params) -> list[RequestOutput]:
+        mine = [i for i in range(len(prompts)) if i % self.dp_size == self.dp_rank]
+        local = self._generate([prompts[i] for i in mine], [sampling_params[i] for i in mine]) if mine else []
+        parts = [None] * self.dp_size
+        torch.distributed.all_gather_object(parts, (mine, local), group=self._dp_group)
+        res = [None] * len(prompts)
+        for idx, outs in parts:
+            for i, o in zip(idx, outs):
+                res[i] = o
+        return res
+
+    def _generate(self, prompts, sampling_params) -> list[RequestOutput]:
         ids = []
         base = self.engine.num_steps * 1_000_003
         for i, (p, sp) in enumerate(zip(prompts, sampling_params)):

@@ -99,6 +99,7 @@ class ParallelState:
     ep: GroupComm = field(default_factory=lambda: GroupComm(None))
     dcp: GroupComm = field(default_factory=lambda: GroupComm(None))
     cpu: dist.ProcessGroup | None = None
+    dp_cpu: dist.ProcessGroup | None = None   # gloo group of this rank's DP peers
     groups: dict = field(default_factory=dict)
 
 
@@ -154,6 +155,11 @@ def initialize_parallel_state(cfg: ParallelConfig) -> ParallelState:
             kv_all.extend(kv)
         st.dcp, _ = _make(kv_all, rank)
     st.cpu = dist.new_group(list(range(W)), backend="gloo")
+    if W // tp > 1:
+        for g in dp_groups(W, tp):
+            pg = dist.new_group(g, backend="gloo")
+            if rank in g:
+                st.dp_cpu = pg
     _STATE = st
     return st
 
