@@ -101,7 +101,8 @@ class LLMEngine:
         self.runner = ModelRunner(self.model, max_num_seqs=args.max_num_seqs,
                                   max_num_batched_tokens=max_tok, max_model_len=self.max_model_len,
                                   block_size=args.block_size,
-                                  cuda_graphs=args.cuda_graphs and self.b200_config.cuda_graphs,
+                                  cuda_graphs=(args.cuda_graphs and self.b200_config.cuda_graphs
+                                               and getattr(self.model, "supports_cuda_graphs", True)),
                                   device=self.device, seed=args.seed)
         nb = args.num_gpu_blocks or self.runner.profile_num_blocks(args.gpu_memory_utilization)
         if real_group and self.device.type == "cuda":
