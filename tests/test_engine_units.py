@@ -135,3 +135,43 @@ def test_prompt_logits_matches_hf():
     with torch.no_grad():
         ref = torch.stack([hf(torch.tensor([p])).logits[0, -1] for p in prompts])
     assert torch.allclose(got, ref, atol=1e-4, rtol=1e-4)
+
+
+def test_block_fp8_checkpoint_loads(tmp_path):
+    """A Llama checkpoint with block-scaled fp8 weights (+ *_scale_inv) loads and matches the
+    dequantized bf16 model's logits."""
+    from safetensors.torch import load_file, save_file
+
+    from tests._tiny import random_prompts, tiny_llama_checkpoint
+    from vllm_neuron_b200.entrypoints import LLM
+    from vllm_neuron_b200.utils.checkpoints import dequant_block_fp8, quant_block_fp8
+    import json, os, shutil
+
+    d, _ = tiny_llama_checkpoint()
+    w = torch.randn(300, 200) * 0.05
+    q, s = quant_block_fp8(w)
+    assert (dequant_block_fp8(q, s, dtype=torch.float32) - w).abs().max() < 0.05 * w.abs().max()
+    out = tmp_path / "fp8"
+    shutil.copytree(d, out)
+    sd = load_file(str(out / "model.safetensors"))
+    deq = {}
+    for n, t in list(sd.items()):
+        if n.endswith("proj.weight") and t.dim() == 2:
+            q, s = quant_block_fp8(t)
+            sd[n], sd[n + "_scale_inv"] = q, s
+            deq[n] = dequant_block_fp8(q, s, dtype=torch.float32)
+    save_file(sd, str(out / "model.safetensors"))
+    cfg = json.load(open(out / "config.json"))
+    cfg["quantization_config"] = {"quant_method": "fp8", "weight_block_size": [128, 128]}
+    json.dump(cfg, open(out / "config.json", "w"))
+    ref_dir = tmp_path / "deq"
+    shutil.copytree(d, ref_dir)
+    sd2 = load_file(str(ref_dir / "model.safetensors"))
+    sd2.update(deq)
+    save_file(sd2, str(ref_dir / "model.safetensors"))
+    kw = dict(device="cpu", dtype="float32", max_num_seqs=4, max_model_len=128, num_gpu_blocks=32,
+              max_num_batched_tokens=128)
+    p = random_prompts(n=2, length=10)
+    a = LLM(str(out), **kw).engine.prompt_logits(p)
+    b = LLM(str(ref_dir), **kw).engine.prompt_logits(p)
+    assert torch.allclose(a, b, atol=1e-5)

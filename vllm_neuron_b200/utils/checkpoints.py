@@ -81,11 +81,56 @@ class SafetensorsCheckpoint:
         return th
 
 
+def dequant_block_fp8(w: torch.Tensor, scale_inv: torch.Tensor, block: tuple[int, int] = (128, 128),
+                      dtype=torch.bfloat16) -> torch.Tensor:
+    """Block-scaled fp8 (e4m3) weight ``[N, K]`` with per-block scales ``[ceil(N/bn), ceil(K/bk)]``
+    -> ``dtype`` (``w * scale`` per block)."""
+    bn, bk = block
+    N, K = w.shape[-2], w.shape[-1]
+    s = scale_inv.float().repeat_interleave(bn, -2)[..., :N, :].repeat_interleave(bk, -1)[..., :K]
+    return (w.float() * s).to(dtype)
+
+
+def quant_block_fp8(w: torch.Tensor, block: tuple[int, int] = (128, 128)) -> tuple[torch.Tensor, torch.Tensor]:
+    """Inverse of :func:`dequant_block_fp8` (amax / 448 per block); builds fp8 checkpoints."""
+    bn, bk = block
+    N, K = w.shape
+    nb, kb = -(-N // bn), -(-K // bk)
+    pad = torch.zeros(nb * bn, kb * bk, dtype=torch.float32)
+    pad[:N, :K] = w.float()
+    blocks = pad.view(nb, bn, kb, bk)
+    scale = blocks.abs().amax(dim=(1, 3)).clamp_min(1e-12) / 448.0
+    q = (blocks / scale[:, None, :, None]).view(nb * bn, kb * bk)[:N, :K].to(torch.float8_e4m3fn)
+    return q, scale
+
+
+def fp8_aware_getter(get, names: set[str], block: tuple[int, int] | None):
+    """Wrap ``get`` so that fp8 weights with a ``*_scale_inv`` (block-scaled, the ModelOpt /
+    DeepSeek / Qwen FP8 layout) are returned dequantized to bf16 (reference: block-FP8 and
+    static FP8 checkpoint handling, vllm_neuron/model/llama3/quantization.py:39-310)."""
+    blk = tuple(block) if block else (128, 128)
+
+    def g(name: str) -> torch.Tensor:
+        t = get(name)
+        if t.dtype in (torch.float8_e4m3fn, torch.float8_e5m2):
+            si = name + "_scale_inv"
+            if si in names:
+                return dequant_block_fp8(t, get(si), blk, torch.float32)
+            sc = name.replace(".weight", ".weight_scale")
+            if sc in names:  # per-tensor static scale
+                return t.float() * get(sc).float()
+            return t.float()
+        return t
+
+    return g
+
+
 def load_checkpoint_into(model, path: str) -> dict:
     t0 = time.perf_counter()
     ck = SafetensorsCheckpoint(path)
     warm = ck.warm_page_cache(model.tp.rank, model.tp.world)
-    model.load_hf_state_dict(ck.get, ck.names())
+    names = ck.names()
+    model.load_hf_state_dict(fp8_aware_getter(ck.get, names, getattr(model.cfg, "weight_block_size", None)), names)
     warm.join(timeout=0)
     if torch.cuda.is_available() and model.device.type == "cuda":
         torch.cuda.synchronize(model.device)
