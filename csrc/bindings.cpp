@@ -550,6 +550,7 @@ void gated_delta_rule(const at::Tensor& qkv, const at::Tensor& z, const at::Tens
   p.Hv = (int)Hv;
   p.dk = (int)state.size(2);
   p.dv = (int)state.size(3);
+  p.T = (int)out.size(0);
   b200::gated_delta_rule_launch(p, linear_batch(q_start, seq_lens, slots), cur_stream());
   check_launch("gated_delta_rule", seq_lens.size(0) > 0 ? 1 : 0);
 }

@@ -13,12 +13,11 @@
 //
 //   causal_conv1d      one thread per channel, a sliding window of K - 1 inputs in registers,
 //                      loads of the step's tokens unrolled so they are in flight together.
-//   gated_delta_rule   one CTA (256 threads) per (sequence, value head); thread (v, half) keeps
-//                      column v, rows [64 * half, 64 * half + 64) of S in registers; per token
-//                      two k-reductions go through shared memory; the gated RMSNorm over dv is
-//                      a CTA reduction.  Tokens are processed in order (the recurrence), with
-//                      the next token's inputs prefetched; the work is spread over
-//                      sequences x heads.
+//   gated_delta_rule   per (sequence, value head, 16 value columns) one CTA of 4 warps; a warp
+//                      keeps 4 columns of S in registers (16 rows per lane) and reduces over
+//                      dk with shuffles, so tokens are processed in order (the recurrence)
+//                      without CTA barriers, next-token inputs prefetched; the gated RMSNorm
+//                      over dv runs afterwards (one warp per token and head).
 #include <cuda_bf16.h>
 
 #include <stdexcept>
@@ -77,22 +76,26 @@ __global__ void __launch_bounds__(128) causal_conv1d_kernel(
   for (int j = 0; j < K - 1; ++j) st[j] = __float2bfloat16(win[j]);
 }
 
-// dk = dv = 128, 256 threads.  The inputs of token i + 1 are loaded while token i is
-// processed (they do not depend on the state), and the shared-memory exchanges use separate
-// buffers per phase so one token costs five CTA barriers.
-__global__ void __launch_bounds__(256) gated_delta_rule_kernel(const GatedDeltaParams p,
+// dk = dv = 128.  The recurrence of value column v only reads column v of S, so columns are
+// independent: a warp owns 4 columns, lane = 8 * c + kg holds rows [16 kg, 16 kg + 16) of
+// column c (16 state floats).  Every k-reduction (the l2 norms of q and k, S^T k and S^T q)
+// is 3 butterfly shuffles inside the warp, so a token costs no CTA barrier; the next token's
+// inputs are loaded while the current one is processed.  Output: the un-normalised o (bf16),
+// normalised afterwards by gated_rmsnorm_kernel.  4 warps per CTA = 16 columns.
+constexpr int kGdnColsPerWarp = 4;
+constexpr int kGdnWarps = 4;
+
+__global__ void __launch_bounds__(128) gated_delta_rule_kernel(const GatedDeltaParams p,
                                                                 LinearAttnBatch bt) {
-  constexpr int DK = 128, DV = 128, R = 64;  // rows of S per thread
+  constexpr int DK = 128, DV = 128, R = 16;
+  constexpr unsigned FULL = 0xffffffffu;
   pdl_trigger();
   pdl_wait();
-  __shared__ float qs[DK], ks[DK];
-  __shared__ float red_kv[2][DV], red_o[2][DV];
-  __shared__ float wsum_qk[8], wsum_o[8];
   const int b = blockIdx.x;
   const int h = blockIdx.y;
-  const int tid = threadIdx.x;
-  const int v = tid & (DV - 1);
-  const int half = tid >> 7;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kg = lane & 7;
+  const int v = (blockIdx.z * kGdnWarps + warp) * kGdnColsPerWarp + (lane >> 3);
   const int kh = h / (p.Hv / p.Hk);
   const int t0 = bt.q_start[b];
   const int n = bt.q_start[b + 1] - t0;
@@ -100,78 +103,114 @@ __global__ void __launch_bounds__(256) gated_delta_rule_kernel(const GatedDeltaP
   float* S = p.state + (long long)bt.slots[b] * p.state_slot_stride + (long long)h * DK * DV;
   float s[R];
 #pragma unroll
-  for (int r = 0; r < R; ++r) s[r] = ctx > 0 ? S[(long long)(half * R + r) * DV + v] : 0.f;
+  for (int r = 0; r < R; ++r) s[r] = ctx > 0 ? S[(long long)(kg * R + r) * DV + v] : 0.f;
   const float A = -__expf(p.A_log[h]);
   const float dtb = p.dt_bias[h];
-  const float nw = __bfloat162float(p.norm_w[v]);
   const float qscale = rsqrtf((float)DK);
-  const int warp = tid >> 5, lane = tid & 31;
-  const int d = tid & (DK - 1);
-  const long long qk_off = (half ? p.Hk * DK : 0) + (long long)kh * DK + d;
-  const long long v_off = 2 * p.Hk * DK + (long long)h * DV + v;
-  const long long z_off = (long long)h * DV + v;
+  const long long q_off = (long long)kh * DK + kg * R;
+  const long long k_off = (long long)p.Hk * DK + q_off;
+  const long long v_off = 2LL * p.Hk * DK + (long long)h * DV + v;
 
-  // per-token inputs of this thread: its q or k element, v element, z element, a, b
-  float n_qk = 0.f, n_v = 0.f, n_z = 0.f, n_a = 0.f, n_b = 0.f;
+  uint4 nq[2], nk[2];
+  float nv = 0.f, na = 0.f, nb = 0.f;
   auto load = [&](long long t) {
-    n_qk = __bfloat162float(p.qkv[t * p.ld_qkv + qk_off]);
-    n_v = __bfloat162float(p.qkv[t * p.ld_qkv + v_off]);
-    n_z = half == 0 ? __bfloat162float(p.z[t * p.ld_zab + z_off]) : 0.f;
-    n_a = __bfloat162float(p.a[t * p.ld_zab + h]);
-    n_b = __bfloat162float(p.b[t * p.ld_zab + h]);
+    const uint4* q4 = reinterpret_cast<const uint4*>(p.qkv + t * p.ld_qkv + q_off);
+    const uint4* k4 = reinterpret_cast<const uint4*>(p.qkv + t * p.ld_qkv + k_off);
+    nq[0] = q4[0];
+    nq[1] = q4[1];
+    nk[0] = k4[0];
+    nk[1] = k4[1];
+    nv = __bfloat162float(p.qkv[t * p.ld_qkv + v_off]);
+    na = __bfloat162float(p.a[t * p.ld_zab + h]);
+    nb = __bfloat162float(p.b[t * p.ld_zab + h]);
   };
   if (n > 0) load(t0);
-
   for (int i = 0; i < n; ++i) {
     const long long t = t0 + i;
-    const float val = n_qk, vt = n_v, zt = n_z, a = n_a, bb = n_b;
-    if (i + 1 < n) load(t + 1);
-    // q (threads 0..127) and k (threads 128..255), l2-normalised over dk
-    const float ss = warp_sum(val * val);
-    if (lane == 0) wsum_qk[warp] = ss;
-    __syncthreads();  // A
-    {
-      const float tot = half ? wsum_qk[4] + wsum_qk[5] + wsum_qk[6] + wsum_qk[7]
-                             : wsum_qk[0] + wsum_qk[1] + wsum_qk[2] + wsum_qk[3];
-      const float inv = rsqrtf(tot + 1e-6f);
-      if (half) ks[d] = val * inv;
-      else qs[d] = val * inv * qscale;
+    float q[R], k[R];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const uint32_t qw[4] = {nq[j].x, nq[j].y, nq[j].z, nq[j].w};
+      const uint32_t kw[4] = {nk[j].x, nk[j].y, nk[j].z, nk[j].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 fq = unpack_bf16x2(qw[e]), fk = unpack_bf16x2(kw[e]);
+        q[8 * j + 2 * e] = fq.x;
+        q[8 * j + 2 * e + 1] = fq.y;
+        k[8 * j + 2 * e] = fk.x;
+        k[8 * j + 2 * e + 1] = fk.y;
+      }
     }
+    const float vt = nv, a = na, bb = nb;
+    if (i + 1 < n) load(t + 1);
+    float sq = 0.f, sk = 0.f;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      sq += q[r] * q[r];
+      sk += k[r] * k[r];
+    }
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) {
+      sq += __shfl_xor_sync(FULL, sq, o);
+      sk += __shfl_xor_sync(FULL, sk, o);
+    }
+    const float iq = rsqrtf(sq + 1e-6f) * qscale, ik = rsqrtf(sk + 1e-6f);
     const float g = __expf(A * softplus_d(a + dtb));
     const float beta = 1.f / (1.f + __expf(-bb));
-    __syncthreads();  // B
     float kv = 0.f;
 #pragma unroll
     for (int r = 0; r < R; ++r) {
+      k[r] *= ik;
       s[r] *= g;
-      kv += s[r] * ks[half * R + r];
+      kv += s[r] * k[r];
     }
-    red_kv[half][v] = kv;
-    __syncthreads();  // C
-    const float delta = (vt - (red_kv[0][v] + red_kv[1][v])) * beta;
-    float o = 0.f;
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) kv += __shfl_xor_sync(FULL, kv, o);
+    const float delta = (vt - kv) * beta;
+    float ov = 0.f;
 #pragma unroll
     for (int r = 0; r < R; ++r) {
-      s[r] += ks[half * R + r] * delta;
-      o += s[r] * qs[half * R + r];
+      s[r] += k[r] * delta;
+      ov += s[r] * q[r];
     }
-    red_o[half][v] = o;
-    __syncthreads();  // E
-    // the recurrence output is rounded to the activation dtype before the gated RMSNorm
-    const float ov = __bfloat162float(__float2bfloat16(red_o[0][v] + red_o[1][v]));
-    const float sq = warp_sum(half == 0 ? ov * ov : 0.f);
-    if (lane == 0) wsum_o[warp] = sq;
-    __syncthreads();  // F
-    if (half == 0) {
-      const float tot = wsum_o[0] + wsum_o[1] + wsum_o[2] + wsum_o[3];
-      const float rstd = rsqrtf(tot / (float)DV + p.eps);
-      // reference order: normalise, cast, scale by the weight, then multiply by silu(z)
-      const float nrm = __bfloat162float(__float2bfloat16(ov * rstd));
-      p.out[t * p.ld_out + (long long)h * DV + v] = __float2bfloat16(nw * nrm * silu_d(zt));
-    }
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) ov += __shfl_xor_sync(FULL, ov, o);
+    if (kg == 0) p.out[t * p.ld_out + (long long)h * DV + v] = __float2bfloat16(ov * iq);
   }
 #pragma unroll
-  for (int r = 0; r < R; ++r) S[(long long)(half * R + r) * DV + v] = s[r];
+  for (int r = 0; r < R; ++r) S[(long long)(kg * R + r) * DV + v] = s[r];
+}
+
+// out[t, h, :] = w * rmsnorm(out[t, h, :]) * silu(z[t, h, :]) over dv = 128 (one warp per row;
+// the normalised value is rounded to bf16 before the weight, as in the reference order).
+__global__ void gated_rmsnorm_kernel(__nv_bfloat16* __restrict__ out, long long ld_out,
+                                     const __nv_bfloat16* __restrict__ z, long long ld_z,
+                                     const __nv_bfloat16* __restrict__ w, int Hv, int rows, float eps) {
+  pdl_trigger();
+  pdl_wait();
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const long long t = row / Hv;
+  const int h = row - (int)t * Hv;
+  __nv_bfloat16* o = out + t * ld_out + (long long)h * 128 + lane * 4;
+  const __nv_bfloat16* zz = z + t * ld_z + (long long)h * 128 + lane * 4;
+  const uint2 ov = *reinterpret_cast<const uint2*>(o);
+  const uint2 zv = *reinterpret_cast<const uint2*>(zz);
+  const uint2 wv = *reinterpret_cast<const uint2*>(w + lane * 4);
+  const float2 o0 = unpack_bf16x2(ov.x), o1 = unpack_bf16x2(ov.y);
+  const float2 z0 = unpack_bf16x2(zv.x), z1 = unpack_bf16x2(zv.y);
+  const float2 w0 = unpack_bf16x2(wv.x), w1 = unpack_bf16x2(wv.y);
+  const float x[4] = {o0.x, o0.y, o1.x, o1.y}, zf[4] = {z0.x, z0.y, z1.x, z1.y},
+              wf[4] = {w0.x, w0.y, w1.x, w1.y};
+  float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
+  ss = warp_sum(ss);
+  const float rstd = rsqrtf(ss / 128.f + eps);
+  float y[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e)
+    y[e] = wf[e] * __bfloat162float(__float2bfloat16(x[e] * rstd)) * silu_d(zf[e]);
+  *reinterpret_cast<uint2*>(o) = make_uint2(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]));
 }
 
 __global__ void sigmoid_gate_mul_kernel(__nv_bfloat16* __restrict__ x, long long ldx,
@@ -210,8 +249,17 @@ void gated_delta_rule_launch(const GatedDeltaParams& p, const LinearAttnBatch& b
   if (p.dk != 128 || p.dv != 128)
     throw std::invalid_argument("gated_delta_rule: head dims must be 128");
   if (p.Hv % p.Hk != 0) throw std::invalid_argument("gated_delta_rule: Hv % Hk != 0");
+  if (p.ld_qkv % 8 != 0 || p.ld_zab % 4 != 0 || p.ld_out % 4 != 0)
+    throw std::invalid_argument("gated_delta_rule: row strides must allow vector loads");
   if (b.B == 0) return;
-  launch_pdl(gated_delta_rule_kernel, dim3(b.B, p.Hv), dim3(256), 0, s, p, b);
+  constexpr int cols_per_cta = kGdnWarps * kGdnColsPerWarp;
+  launch_pdl(gated_delta_rule_kernel, dim3(b.B, p.Hv, 128 / cols_per_cta), dim3(32 * kGdnWarps), 0,
+             s, p, b);
+  // rows of this step: tokens x value heads (token count from the host-side sizes)
+  const int rows = p.T * p.Hv;
+  if (rows > 0)
+    launch_pdl(gated_rmsnorm_kernel, dim3((rows + 7) / 8), dim3(256), 0, s, p.out, p.ld_out, p.z,
+               p.ld_zab, p.norm_w, p.Hv, rows, p.eps);
 }
 
 void sigmoid_gate_mul_launch(__nv_bfloat16* x, long long ldx, const __nv_bfloat16* gate,

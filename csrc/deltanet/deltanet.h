@@ -41,6 +41,7 @@ struct GatedDeltaParams {
   __nv_bfloat16* out;         // [T, Hv * dv]
   long long ld_out;
   int Hk, Hv, dk, dv;
+  int T;                      // tokens of this step (rows of out)
 };
 
 // Recurrent gated delta rule over this step's tokens (q, k l2-normalised, q scaled by
