@@ -75,3 +75,15 @@ def test_async_scheduling_matches_sync():
     assert [o.outputs[0].token_ids for o in got] == [o.outputs[0].token_ids for o in ref]
     assert got[1].outputs[0].finish_reason == "stop"
     assert len(asy.engine._free_slots) == asy.engine.runner.max_slots - 1
+
+
+def test_prompt_embeds_match_token_prompts():
+    """Passing the embedding rows of a prompt instead of its ids gives the same generation."""
+    d, hf = tiny_llama_checkpoint()
+    prompts = random_prompts(n=2, length=20)
+    sp = SamplingParams(temperature=0, max_tokens=6, ignore_eos=True)
+    llm = LLM(d, device="cpu", max_num_seqs=4, max_model_len=128, num_gpu_blocks=32, max_num_batched_tokens=16)
+    ref = llm.generate(prompts, sp)
+    emb = hf.get_input_embeddings().weight.detach()
+    got = llm.generate([{"prompt_embeds": emb[torch.tensor(p)]} for p in prompts], sp)
+    assert [o.outputs[0].token_ids for o in got] == [o.outputs[0].token_ids for o in ref]

@@ -121,6 +121,11 @@ class LLM:
         ids = []
         base = self.engine.num_steps * 1_000_003
         for i, (p, sp) in enumerate(zip(prompts, sampling_params)):
+            if isinstance(p, dict) and "prompt_embeds" in p:
+                emb = p["prompt_embeds"]
+                ids.append(self.engine.add_request([0] * emb.shape[0], sp, request_id=f"gen-{base}-{i}",
+                                                   prompt_embeds=emb))
+                continue
             toks = _normalize_prompt(p, self.tokenizer)
             ids.append(self.engine.add_request(toks, sp, request_id=f"gen-{base}-{i}"))
         done = {r.request_id: r for r in self.engine.run_until_done()}

@@ -54,6 +54,8 @@ class ForwardBatch:
     last_tok: torch.Tensor | None = None  # device-resident tokens for ids < 0
     seq_slots: torch.Tensor | None = None  # [B] int32 per-request state-cache slots
     want_hidden: bool = False  # return the final-norm hidden states of the logits rows (pooling)
+    embed_rows: torch.Tensor | None = None   # [n] int64 batch rows whose embeddings are given
+    embeds: torch.Tensor | None = None       # [n, H] the given embeddings (prompt_embeds)
 
 
 def _shard(n: int, world: int, rank: int) -> tuple[int, int]:
@@ -204,6 +206,8 @@ class LlamaForCausalLM(torch.nn.Module):
         ops.embedding(b.input_ids, self.embed, self.vocab_start, self.vocab_start + self.V_local, out=res,
                       last_tok=b.last_tok)
         tp.all_reduce_(res)
+        if b.embed_rows is not None:
+            res.index_copy_(0, b.embed_rows, b.embeds.to(res.dtype))
         ops.rmsnorm(res, self.layers[0].input_norm, self.eps, out=x)
         nL = len(self.layers)
         for i, ly in enumerate(self.layers):

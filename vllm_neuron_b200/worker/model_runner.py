@@ -248,6 +248,21 @@ class ModelRunner:
         self._last_work_len = len(w.work)
         return s, w.decode, w.num_splits
 
+    def _attach_prompt_embeds(self, out: SchedulerOutput, fb: ForwardBatch):
+        """Rows of this step that are prompt positions of requests with ``prompt_embeds``."""
+        rows, parts = [], []
+        t = 0
+        for sr in out.scheduled:
+            emb = sr.req.prompt_embeds
+            if emb is not None and sr.start < sr.req.num_prompt_tokens:
+                end = min(sr.start + sr.num_tokens, sr.req.num_prompt_tokens)
+                rows.extend(range(t, t + end - sr.start))
+                parts.append(emb[sr.start:end])
+            t += sr.num_tokens
+        if rows:
+            fb.embed_rows = torch.tensor(rows, dtype=torch.long).to(self.device, non_blocking=True)
+            fb.embeds = torch.cat(parts, 0).to(self.device, non_blocking=True)
+
     def _snapshot(self, out: SchedulerOutput, lay: Layout, decode: bool, splits: int):
         """Save one step's device inputs (the packed int32 buffer and its layout)."""
         import os
@@ -385,6 +400,7 @@ class ModelRunner:
             self.h2d_bytes += n * 4
             fb, samp = self._views(dev, lay, B, S, W, decode, splits)
             fb.work = fb.work[:W]
+            self._attach_prompt_embeds(out, fb)
             if S > 0:
                 mask = bitmask.to(self.device, non_blocking=True) if bitmask is not None else None
                 self._forward_and_sample(fb, samp, S, self.tok_dev, self.lp_dev, mask)
