@@ -580,6 +580,25 @@ void apply_token_bitmask(at::Tensor& logits, const at::Tensor& mask) {
   check_launch("apply_token_bitmask", logits.size(0) > 0 ? 1 : 0);
 }
 
+void moe_mxfp4_gemm(const at::Tensor& x, const at::Tensor& wq, const at::Tensor& ws, at::Tensor& out,
+                    const at::Tensor& gtiles, const at::Tensor& gcount) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  CHECK_BF16(out);
+  TORCH_CHECK(wq.scalar_type() == at::kByte && ws.scalar_type() == at::kByte && wq.dim() == 3 &&
+                  ws.dim() == 3 && wq.is_contiguous() && ws.is_contiguous(),
+              "moe_mxfp4_gemm: wq [E, N, K/2] and ws [E, N, K/32] uint8");
+  const int K = (int)wq.size(2) * 2;
+  TORCH_CHECK(x.size(1) == K && ws.size(2) * 32 == K && out.size(1) == wq.size(1), "moe_mxfp4_gemm: shapes");
+  TORCH_CHECK(x.stride(1) == 1 && out.stride(1) == 1, "moe_mxfp4_gemm: layouts");
+  const c10::cuda::CUDAGuard guard(x.device());
+  b200::moe_mxfp4_gemm_launch(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0),
+                              wq.data_ptr<uint8_t>(), ws.data_ptr<uint8_t>(), gtiles.data_ptr<int>(),
+                              gcount.data_ptr<int>(), (int)gtiles.size(0), (int)wq.size(1), K,
+                              reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0), cur_stream());
+  check_launch("moe_mxfp4_gemm");
+}
+
 int64_t num_sms() { return b200::num_sms_cached(); }
 int64_t launch_count() { return g_launches.load(); }
 
@@ -611,6 +630,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_gather", &moe_gather);
   m.def("moe_act", &moe_act);
   m.def("moe_combine", &moe_combine);
+  m.def("moe_mxfp4_gemm", &moe_mxfp4_gemm);
   m.def("causal_conv1d", &causal_conv1d);
   m.def("gated_delta_rule", &gated_delta_rule);
   m.def("sigmoid_gate_mul", &sigmoid_gate_mul);

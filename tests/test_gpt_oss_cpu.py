@@ -70,3 +70,29 @@ def test_mxfp4_roundtrip_matches_transformers_dequant():
     ref = convert_moe_packed_tensors(blocks, scales, dtype=torch.float32)
     # transformers returns the transposed [..., K, N] layout of the HF module
     assert torch.equal(ref.transpose(-1, -2).contiguous(), deq) or torch.equal(ref, deq)
+
+
+def test_mxfp4_kernel_layout_roundtrip():
+    """Emulate the MXFP4 kernel's fragment reads (lane t, 64-k chunk c: bytes 8t..8t+7 of the
+    repacked row hold k = 16s + 2t, +1 (byte 2s) and 16s + 2t + 8, +9 (byte 2s + 1))."""
+    from vllm_neuron_b200.models.gpt_oss import _FP4_VALUES, dequant_mxfp4, quant_mxfp4
+    from vllm_neuron_b200.ops.moe import pack_mxfp4
+
+    w = torch.randn(2, 5, 128) * 0.3
+    blocks, scales = quant_mxfp4(w)
+    ref = dequant_mxfp4(blocks, scales, torch.float32)
+    wq, ws = pack_mxfp4(blocks, scales)
+    lut = torch.tensor(_FP4_VALUES)
+    got = torch.zeros_like(ref)
+    for e in range(2):
+        for n in range(5):
+            for c in range(2):
+                for t in range(4):
+                    by = wq[e, n, c * 32 + 8 * t:c * 32 + 8 * t + 8].tolist()
+                    for s in range(4):
+                        sc = 2.0 ** (int(ws[e, n, 2 * c + s // 2]) - 127)
+                        for half, b in enumerate((by[2 * s], by[2 * s + 1])):
+                            k = c * 64 + 16 * s + 2 * t + 8 * half
+                            got[e, n, k] = lut[b & 15] * sc
+                            got[e, n, k + 1] = lut[b >> 4] * sc
+    assert torch.equal(got, ref)

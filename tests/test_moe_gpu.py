@@ -88,3 +88,27 @@ def test_moe_block_shared_expert(cuda_device, T):
     ids, w = M.route_ref(logits[:, :E], k, M.ROUTE_SOFTMAX_TOPK, True)
     ref = M.experts_ref(x, ids, w, w_gu, w_dn) + torch.sigmoid(logits[:, E:].float()) * M.shared_expert_ref(x, s_gu, s_dn)
     assert _rel_err(out, ref) < 2e-2
+
+
+@pytest.mark.parametrize("T", [1, 5, 32])
+def test_moe_block_mxfp4_decode(cuda_device, T):
+    """GPT-OSS-style block with MXFP4 experts: the fp4 decode kernel against the fp32 oracle of
+    the same (dequantized) weights."""
+    from vllm_neuron_b200.models.gpt_oss import dequant_mxfp4, quant_mxfp4
+
+    E, k, H, I = 32, 4, 2880 // 2, 2880 // 2
+    g = torch.Generator(device=cuda_device).manual_seed(3)
+    x = torch.randn(T, H, device=cuda_device, generator=g).to(torch.bfloat16)
+    rw = (torch.randn(E, H, device=cuda_device, generator=g) * 0.05).to(torch.bfloat16)
+    gu_b, gu_s = quant_mxfp4(torch.randn(E, 2 * I, H, generator=torch.Generator().manual_seed(4)) * H ** -0.5)
+    dn_b, dn_s = quant_mxfp4(torch.randn(E, H, I, generator=torch.Generator().manual_seed(5)) * I ** -0.5)
+    w_gu = dequant_mxfp4(gu_b, gu_s).to(cuda_device)
+    w_dn = dequant_mxfp4(dn_b, dn_s).to(cuda_device)
+    fp4_gu = tuple(t.to(cuda_device) for t in M.pack_mxfp4(gu_b, gu_s))
+    fp4_dn = tuple(t.to(cuda_device) for t in M.pack_mxfp4(dn_b, dn_s))
+    ws = M.MoEWorkspace.create(64, k, E, E, H, I, cuda_device)
+    out = M.moe_block(x, rw, w_gu, w_dn, k, M.ROUTE_TOPK_SOFTMAX, act=M.ACT_GPTOSS, ws=ws,
+                      fp4_gu=fp4_gu, fp4_down=fp4_dn)
+    ids, w = M.route_ref(ws.logits[:T, :E], k, M.ROUTE_TOPK_SOFTMAX)
+    ref = M.experts_ref(x, ids, w, w_gu, w_dn, act=M.ACT_GPTOSS)
+    assert _rel_err(out, ref) < 2e-2

@@ -29,30 +29,40 @@ _FP4_VALUES = [0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0, -0.0, -0.5, -1.0, -1.5, -
 def dequant_mxfp4(blocks: torch.Tensor, scales: torch.Tensor, dtype=torch.bfloat16) -> torch.Tensor:
     """``blocks [..., G, 16]`` uint8 (two e2m1 values per byte, low nibble first) and
     ``scales [..., G]`` uint8 (e8m0, bias 127) -> ``[..., G * 32]``."""
-    lut = torch.tensor(_FP4_VALUES, dtype=torch.float32)
+    lut = torch.tensor(_FP4_VALUES, dtype=torch.float32, device=blocks.device)
     b = blocks.to(torch.int64)
     lo = lut[b & 0x0F]
     hi = lut[b >> 4]
     v = torch.stack([lo, hi], dim=-1).reshape(*blocks.shape[:-1], 32)
     e = scales.to(torch.int32) - 127
-    v = v * torch.pow(2.0, e.to(torch.float32))[..., None]
+    v = v * torch.pow(torch.tensor(2.0, device=blocks.device), e.to(torch.float32))[..., None]
     return v.reshape(*blocks.shape[:-2], blocks.shape[-2] * 32).to(dtype)
 
 
 def quant_mxfp4(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """Round ``w [..., K]`` (K % 32 == 0) to MXFP4: returns ``(blocks [..., K/32, 16], scales)``.
     Used to build random MXFP4 experts with the checkpoint format."""
-    lut = torch.tensor(_FP4_VALUES[:8], dtype=torch.float32)
+    lut = torch.tensor(_FP4_VALUES[:8], dtype=torch.float32, device=w.device)
     x = w.float().reshape(*w.shape[:-1], w.shape[-1] // 32, 32)
     amax = x.abs().amax(-1).clamp_min(1e-30)
     e = torch.clamp(torch.ceil(torch.log2(amax / 6.0)), -127, 127)
-    scaled = x / torch.pow(2.0, e)[..., None]
+    scaled = x / torch.pow(torch.tensor(2.0, device=w.device), e)[..., None]
     mag = scaled.abs().clamp(max=6.0)
     idx = (mag[..., None] - lut).abs().argmin(-1)
     code = idx | ((scaled < 0).to(torch.int64) << 3)
     code = code.reshape(*code.shape[:-1], 16, 2)
     blocks = (code[..., 0] | (code[..., 1] << 4)).to(torch.uint8)
     return blocks, (e + 127).to(torch.uint8)
+
+
+def _quant_experts(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """MXFP4-quantize ``w [E, N, K]`` expert by expert (bounded temporary memory)."""
+    bl, sc = [], []
+    for e in range(w.shape[0]):
+        b, s = quant_mxfp4(w[e])
+        bl.append(b)
+        sc.append(s)
+    return torch.stack(bl), torch.stack(sc)
 
 
 class GptOssForCausalLM(LlamaForCausalLM):
@@ -75,6 +85,11 @@ class GptOssForCausalLM(LlamaForCausalLM):
         if self.device.type == "cuda":
             self.moe_ws = M.MoEWorkspace.create(self.max_tokens, self.topk, self.E, self.e_local, self.H,
                                                 self.I_moe, self.device)
+        # MXFP4 copies of the experts for decode-sized batches (K = H for gate/up, I for down
+        # must be multiples of 64); the bf16 copies serve prefill.
+        self.use_fp4 = self.device.type == "cuda" and self.H % 64 == 0 and self.I_moe % 64 == 0
+        for ly in self.layers:
+            ly.fp4_gu = ly.fp4_down = None
 
     def _make_mlp(self, m, p, layer: int):
         m.router = p(self.E, self.H)
@@ -85,13 +100,29 @@ class GptOssForCausalLM(LlamaForCausalLM):
         m.w_down = p(self.e_local, self.H, self.I_moe)
         m.b_down = p(self.e_local, self.H)
 
+    @torch.no_grad()
+    def set_expert_mxfp4(self, ly, gu_blocks=None, gu_scales=None, dn_blocks=None, dn_scales=None):
+        """Install the layer's MXFP4 experts: from checkpoint blocks/scales (gate/up rows in
+        this model's gate-then-up order), or by quantizing the current bf16 weights; the bf16
+        copies are set to the dequantized values so prefill and decode use the same weights."""
+        if not self.use_fp4:
+            return
+        if gu_blocks is None:
+            gu_blocks, gu_scales = _quant_experts(ly.w_gu)
+            dn_blocks, dn_scales = _quant_experts(ly.w_down)
+        ly.w_gu.copy_(dequant_mxfp4(gu_blocks, gu_scales).to(ly.w_gu.device))
+        ly.w_down.copy_(dequant_mxfp4(dn_blocks, dn_scales).to(ly.w_down.device))
+        ly.fp4_gu = tuple(t.to(self.device) for t in M.pack_mxfp4(gu_blocks, gu_scales))
+        ly.fp4_down = tuple(t.to(self.device) for t in M.pack_mxfp4(dn_blocks, dn_scales))
+
     def _mlp(self, i, ly, x, res, nxt_norm, T, small, fused):
         h = self.ws_h[:T]
         M.moe_block(x, ly.router, ly.w_gu, ly.w_down, self.topk, M.ROUTE_TOPK_SOFTMAX,
                     router_b=ly.router_bias, b_gu=ly.b_gu,
                     b_down=ly.b_down,  # each assignment is computed on exactly one rank
                     act=M.ACT_GPTOSS, alpha=self.cfg.swiglu_alpha, limit=self.cfg.swiglu_limit,
-                    e_start=self.e_start, ws=self.moe_ws, out=h)
+                    e_start=self.e_start, ws=self.moe_ws, out=h, fp4_gu=ly.fp4_gu,
+                    fp4_down=ly.fp4_down)
         self.tp.all_reduce_(h)
         ops.add_rmsnorm(h, res, nxt_norm, self.eps, out=x)
 
@@ -102,6 +133,7 @@ class GptOssForCausalLM(LlamaForCausalLM):
         g.manual_seed(seed * 1000 + 7 + self.tp.rank)
         for ly in self.layers:
             ly.sinks.normal_(0.0, 1.0, generator=g)
+            self.set_expert_mxfp4(ly)
 
     def load_hf_state_dict(self, get_tensor, names: set[str]):
         from ..utils.weight_loader import load_gpt_oss

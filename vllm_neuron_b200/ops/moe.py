@@ -164,6 +164,24 @@ def route(logits: torch.Tensor, k: int, mode: int, renorm: bool = True,
     return ids, weights
 
 
+def pack_mxfp4(blocks: torch.Tensor, scales: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Checkpoint MXFP4 ``blocks [..., N, K/32, 16]`` / ``scales [..., N, K/32]`` -> the kernel
+    layout ``wq [..., N, K/2]`` (inside every 32-byte group, byte ``8t + j`` = original byte
+    ``t + 4j``: the order lane t of an m16n8k16 B fragment consumes) and ``ws [..., N, K/32]``."""
+    *lead, N, G, _ = blocks.shape
+    b = blocks.reshape(*lead, N, G * 16)
+    K2 = G * 16
+    assert K2 % 32 == 0, "K must be a multiple of 64"
+    v = b.reshape(*lead, N, K2 // 32, 8, 4)            # [.., chunk, j, t] = byte t + 4j
+    wq = v.transpose(-1, -2).reshape(*lead, N, K2)     # [.., chunk, t, j] -> byte 8t + j
+    return wq.contiguous(), scales.reshape(*lead, N, G).contiguous()
+
+
+def mxfp4_gemm_ref(x: torch.Tensor, rows_expert: torch.Tensor, w_bf16: torch.Tensor) -> torch.Tensor:
+    """fp32 oracle of the grouped MXFP4 matmul: row r uses expert ``rows_expert[r]``."""
+    return torch.einsum("rk,rnk->rn", x.float(), w_bf16[rows_expert.long()].float())
+
+
 def shared_expert_ref(x: torch.Tensor, w_gu: torch.Tensor, w_down: torch.Tensor) -> torch.Tensor:
     I = w_gu.shape[0] // 2
     h = x.float() @ w_gu.float().t()
@@ -176,7 +194,8 @@ def moe_block(x: torch.Tensor, router_w: torch.Tensor, w_gu: torch.Tensor, w_dow
               act: int = ACT_SILU, alpha: float = 1.702, limit: float = 7.0, e_start: int = 0,
               ws: MoEWorkspace | None = None, out: torch.Tensor | None = None,
               num_experts: int | None = None, shared_gu: torch.Tensor | None = None,
-              shared_down: torch.Tensor | None = None) -> torch.Tensor:
+              shared_down: torch.Tensor | None = None, fp4_gu: tuple | None = None,
+              fp4_down: tuple | None = None, fp4_max_tokens: int = 64) -> torch.Tensor:
     """Routed experts for ``x [T, H]`` (see the module docstring); returns ``out [T, H]`` bf16.
 
     ``w_gu [e_local, 2I, H]`` holds each expert's gate rows followed by its up rows,
@@ -225,11 +244,18 @@ def moe_block(x: torch.Tensor, router_w: torch.Tensor, w_gu: torch.Tensor, w_dow
     xp = ws.xp[:R]
     ext().moe_gather(x, ws.sorted_src, k, ws.offsets, xp)
     gu = ws.gu[:R]
-    ext().gemm_grouped(xp, w_gu, gu, ws.gtiles, ws.gcount, EPI_BF16, 256)
+    use_fp4 = fp4_gu is not None and T <= fp4_max_tokens
+    if use_fp4:
+        ext().moe_mxfp4_gemm(xp, fp4_gu[0], fp4_gu[1], gu, ws.gtiles, ws.gcount)
+    else:
+        ext().gemm_grouped(xp, w_gu, gu, ws.gtiles, ws.gcount, EPI_BF16, 256)
     a = ws.act[:R, :I]
     ext().moe_act(gu, b_gu, ws.row_expert, ws.offsets, act, alpha, limit, a)
     y = ws.y[:R]
-    ext().gemm_grouped(a, w_down, y, ws.gtiles, ws.gcount, EPI_BF16, 256 if H % 256 == 0 else 128)
+    if use_fp4:
+        ext().moe_mxfp4_gemm(a, fp4_down[0], fp4_down[1], y, ws.gtiles, ws.gcount)
+    else:
+        ext().gemm_grouped(a, w_down, y, ws.gtiles, ws.gcount, EPI_BF16, 256 if H % 256 == 0 else 128)
     ext().moe_combine(y, ws.inv_pos[:R], w, ids, b_down, e_start, shared,
                       ws.shared_gate[:T] if has_shared else None, out)
     return out

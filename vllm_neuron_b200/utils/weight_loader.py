@@ -154,6 +154,15 @@ def load_gpt_oss(model, get_tensor: Callable[[str], torch.Tensor], names: set[st
             dn = _expert_tensor(get_tensor, names, dn_name)[e0:e0 + el]
         _copy(ly.w_down, dn, p + "w_down")
         _copy(ly.b_down, get_tensor(dn_name + "_bias")[e0:e0 + el], p + "b_down")
+        # MXFP4 checkpoints keep their experts in MXFP4 for decode; bf16 checkpoints stay bf16
+        if getattr(model, "use_fp4", False):
+            if gu_name + "_blocks" in names:
+                gb = get_tensor(gu_name + "_blocks")[e0:e0 + el]
+                gs = get_tensor(gu_name + "_scales")[e0:e0 + el]
+                model.set_expert_mxfp4(ly, torch.cat([gb[:, 0::2], gb[:, 1::2]], 1),
+                                       torch.cat([gs[:, 0::2], gs[:, 1::2]], 1),
+                                       get_tensor(dn_name + "_blocks")[e0:e0 + el],
+                                       get_tensor(dn_name + "_scales")[e0:e0 + el])
     _copy(model.final_norm, get_tensor(pre + "norm.weight"), "norm")
     _copy(model.lm_head, shard_rows(get_tensor("lm_head.weight"), W, r, model.V_local), "lm_head")
 
