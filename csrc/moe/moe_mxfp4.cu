@@ -11,11 +11,11 @@
 // mma.m16n8k16 B fragment consumes k = 16s + 2t (+1) and 16s + 2t + 8 (+9) for slices s = 0..3,
 // so each lane fetches its weights of a 64-k chunk with one 8-byte load.  Scales: [E, N, K/32].
 //
-// A CTA (4 warps) owns one entry of the moe_align tile list (<= 16 rows of one expert per
-// pass) and 128 output columns; the entry's X rows sit in shared memory for the whole K loop,
+// A CTA (8 warps) owns one entry of the moe_align tile list (<= 16 rows of one expert per
+// pass) and 256 output columns; the entry's X rows sit in shared memory for the whole K loop,
 // each warp streams the fp4 weights of its 32 columns (next chunk's loads in flight while the
-// current chunk is converted in registers to bf16 x 2^(scale - 127), exact) and accumulates
-// with mma.sync m16n8k16 (the rows are tokens; a tensor-core tile of tokens x 8 columns).
+// current chunk is converted) and accumulates with mma.sync m16n8k16 (the rows are tokens; a
+// tensor-core tile of tokens x 8 columns).
 #include <cuda_bf16.h>
 
 #include <stdexcept>
@@ -48,26 +48,28 @@ __device__ __forceinline__ uint32_t fp4_to_bf16_bits(uint32_t x) {
   const uint32_t mag = e ? (((e + 126u) << 7) | (m << 6)) : (m ? 0x3F00u : 0u);
   return sign | mag;
 }
-// Two nibbles of one byte -> bf16x2 scaled by 2^(s - 127) (multiplication in fp32; exact).
-__device__ __forceinline__ uint32_t fp4x2_to_bf16x2(uint32_t byte, float scale) {
-  const float lo = __uint_as_float(fp4_to_bf16_bits(byte & 15u) << 16) * scale;
-  const float hi = __uint_as_float(fp4_to_bf16_bits(byte >> 4) << 16) * scale;
-  return pack_bf16x2(lo, hi);
-}
 
 constexpr int kRows = 16;    // token rows per pass
-constexpr int kCols = 128;   // output columns per CTA (4 warps x 32)
+constexpr int kWarpsMx = 8;  // warps per CTA (32 output columns each)
+constexpr int kCols = 32 * kWarpsMx;
 constexpr int kPadK = 8;     // X row padding (halves) against ldmatrix bank conflicts
 
 }  // namespace
 
-__global__ void __launch_bounds__(128) moe_mxfp4_gemm_kernel(
+// Dequantisation: a 256-entry shared-memory table maps one byte (two e2m1 nibbles) to the
+// bf16x2 pair of their unscaled values (one shared load per two weights); the e8m0 block
+// scale is applied after the tensor-core product of each 32-k block (tmp accumulator, then
+// acc += 2^(s-127) * tmp), so no per-weight multiply is needed.
+__global__ void __launch_bounds__(32 * kWarpsMx) moe_mxfp4_gemm_kernel(
     const __nv_bfloat16* __restrict__ x, long long ldx, const uint8_t* __restrict__ wq,
     const uint8_t* __restrict__ ws, const int4* __restrict__ gtiles, const int* __restrict__ gcount,
     int N, int K, __nv_bfloat16* __restrict__ y, long long ldy) {
   pdl_trigger();
-  pdl_wait();
+  __shared__ uint32_t lut[256];
   extern __shared__ __align__(16) uint8_t smem_x[];
+  for (int i = threadIdx.x; i < 256; i += blockDim.x)
+    lut[i] = fp4_to_bf16_bits(i & 15u) | (fp4_to_bf16_bits(i >> 4) << 16);
+  pdl_wait();
   const int entry = blockIdx.x;
   if (entry >= *gcount) return;
   const int4 g = gtiles[entry];
@@ -83,7 +85,7 @@ __global__ void __launch_bounds__(128) moe_mxfp4_gemm_kernel(
 
   for (int r0 = row0; r0 < row_end; r0 += kRows) {
     const int nr = min(kRows, row_end - r0);
-    __syncthreads();  // previous pass done with the X tile
+    __syncthreads();  // LUT ready / previous pass done with the X tile
     for (int i = threadIdx.x; i < kRows * (K / 8); i += blockDim.x) {
       const int r = i / (K / 8), c = i % (K / 8);
       uint4 v = make_uint4(0, 0, 0, 0);
@@ -95,7 +97,6 @@ __global__ void __launch_bounds__(128) moe_mxfp4_gemm_kernel(
     float acc[4][4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-    // column n of n-tile j for this lane's B fragment
     int ncol[4];
     bool nok[4];
 #pragma unroll
@@ -103,9 +104,11 @@ __global__ void __launch_bounds__(128) moe_mxfp4_gemm_kernel(
       ncol[j] = n_base + 8 * j + grp;
       nok[j] = ncol[j] < N;
     }
+    // the scales of the D fragment's columns (2t, 2t + 1 of each n-tile) come from lanes
+    // grp' = 2t and 2t + 1 of the same n-tile (they load the scale of column grp')
     const int nchunks = K / 64;
     uint2 wb[4];
-    uint16_t sb[4];
+    uint32_t sb[4];
     auto load_w = [&](int c) {
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -121,14 +124,13 @@ __global__ void __launch_bounds__(128) moe_mxfp4_gemm_kernel(
     load_w(0);
     for (int c = 0; c < nchunks; ++c) {
       uint2 cw[4];
-      uint16_t cs[4];
+      uint32_t cs[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         cw[j] = wb[j];
         cs[j] = sb[j];
       }
       if (c + 1 < nchunks) load_w(c + 1);
-      // A fragments of the 4 k16 slices of this chunk
       uint32_t a[4][4];
 #pragma unroll
       for (int s = 0; s < 4; ++s) {
@@ -138,17 +140,25 @@ __global__ void __launch_bounds__(128) moe_mxfp4_gemm_kernel(
       }
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const float sc0 = __uint_as_float(((uint32_t)(cs[j] & 0xFF)) << 23);
-        const float sc1 = __uint_as_float(((uint32_t)(cs[j] >> 8)) << 23);
-        const uint32_t w4[2] = {cw[j].x, cw[j].y};
+        // scales of output columns 2t and 2t + 1: held by lanes (2t) * 4 + t' and (2t + 1) * 4
+        const uint32_t sc_lo = __shfl_sync(0xffffffffu, cs[j], (2 * t) * 4);
+        const uint32_t sc_hi = __shfl_sync(0xffffffffu, cs[j], (2 * t + 1) * 4);
 #pragma unroll
-        for (int s = 0; s < 4; ++s) {
-          // bytes 2s (b0: k = 16s + 2t, +1) and 2s + 1 (b1: k = 16s + 2t + 8, +9)
-          const int jb = 2 * s;
-          const uint32_t byte0 = (w4[jb >> 2] >> (8 * (jb & 3))) & 0xFFu;
-          const uint32_t byte1 = (w4[(jb + 1) >> 2] >> (8 * ((jb + 1) & 3))) & 0xFFu;
-          const float sc = s < 2 ? sc0 : sc1;
-          mma_bf16(acc[j], a[s], fp4x2_to_bf16x2(byte0, sc), fp4x2_to_bf16x2(byte1, sc));
+        for (int hb = 0; hb < 2; ++hb) {  // 32-k block of the chunk
+          float tmp[4] = {0.f, 0.f, 0.f, 0.f};
+          const uint32_t w = hb ? cw[j].y : cw[j].x;
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {  // slice s = 2 hb + q: bytes 2q, 2q + 1 of w
+            const uint32_t b0 = lut[(w >> (16 * q)) & 0xFFu];
+            const uint32_t b1 = lut[(w >> (16 * q + 8)) & 0xFFu];
+            mma_bf16(tmp, a[2 * hb + q], b0, b1);
+          }
+          const float s0 = __uint_as_float(((sc_lo >> (8 * hb)) & 0xFFu) << 23);
+          const float s1 = __uint_as_float(((sc_hi >> (8 * hb)) & 0xFFu) << 23);
+          acc[j][0] += s0 * tmp[0];
+          acc[j][1] += s1 * tmp[1];
+          acc[j][2] += s0 * tmp[2];
+          acc[j][3] += s1 * tmp[3];
         }
       }
     }
@@ -180,7 +190,7 @@ void moe_mxfp4_gemm_launch(const __nv_bfloat16* x, long long ldx, const uint8_t*
   if (smem > 227 * 1024) throw std::invalid_argument("moe_mxfp4_gemm: K too large for the X tile");
   static std::atomic<uint64_t> configured{0};
   set_max_dynamic_smem_once(moe_mxfp4_gemm_kernel, smem, configured);
-  launch_pdl(moe_mxfp4_gemm_kernel, dim3(gmax, (N + kCols - 1) / kCols), dim3(128), smem, s, x, ldx,
+  launch_pdl(moe_mxfp4_gemm_kernel, dim3(gmax, (N + kCols - 1) / kCols), dim3(32 * kWarpsMx), smem, s, x, ldx,
              wq, ws, reinterpret_cast<const int4*>(gtiles), gcount, N, K, y, ldy);
 }
 

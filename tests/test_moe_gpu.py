@@ -96,7 +96,7 @@ def test_moe_block_mxfp4_decode(cuda_device, T):
     the same (dequantized) weights."""
     from vllm_neuron_b200.models.gpt_oss import dequant_mxfp4, quant_mxfp4
 
-    E, k, H, I = 32, 4, 2880 // 2, 2880 // 2
+    E, k, H, I = 32, 4, 1536, 1344  # K of both matmuls a multiple of 64
     g = torch.Generator(device=cuda_device).manual_seed(3)
     x = torch.randn(T, H, device=cuda_device, generator=g).to(torch.bfloat16)
     rw = (torch.randn(E, H, device=cuda_device, generator=g) * 0.05).to(torch.bfloat16)
