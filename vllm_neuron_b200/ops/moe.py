@@ -245,15 +245,17 @@ def moe_block(x: torch.Tensor, router_w: torch.Tensor, w_gu: torch.Tensor, w_dow
     ext().moe_gather(x, ws.sorted_src, k, ws.offsets, xp)
     gu = ws.gu[:R]
     use_fp4 = fp4_gu is not None and T <= fp4_max_tokens
+    # every tile-list entry holds >= 1 row: at most R entries exist (bounds the fp4 grid)
+    gt = ws.gtiles[:min(ws.gtiles.shape[0], R)]
     if use_fp4:
-        ext().moe_mxfp4_gemm(xp, fp4_gu[0], fp4_gu[1], gu, ws.gtiles, ws.gcount)
+        ext().moe_mxfp4_gemm(xp, fp4_gu[0], fp4_gu[1], gu, gt, ws.gcount)
     else:
         ext().gemm_grouped(xp, w_gu, gu, ws.gtiles, ws.gcount, EPI_BF16, 256)
     a = ws.act[:R, :I]
     ext().moe_act(gu, b_gu, ws.row_expert, ws.offsets, act, alpha, limit, a)
     y = ws.y[:R]
     if use_fp4:
-        ext().moe_mxfp4_gemm(a, fp4_down[0], fp4_down[1], y, ws.gtiles, ws.gcount)
+        ext().moe_mxfp4_gemm(a, fp4_down[0], fp4_down[1], y, gt, ws.gcount)
     else:
         ext().gemm_grouped(a, w_down, y, ws.gtiles, ws.gcount, EPI_BF16, 256 if H % 256 == 0 else 128)
     ext().moe_combine(y, ws.inv_pos[:R], w, ids, b_down, e_start, shared,
