@@ -138,11 +138,44 @@ def bench_prefill_attention(tp: int):
     return rows
 
 
+def bench_moe(tp: int):
+    """GPT-OSS-20B expert block (32 experts top-4, hidden 2880, FFN 2880) at decode batch sizes:
+    bf16 grouped tcgen05 GEMMs against the MXFP4 decode kernel (same routing, same weights)."""
+    from vllm_neuron_b200.models.gpt_oss import _quant_experts, dequant_mxfp4
+    from vllm_neuron_b200.ops import moe as M
+
+    E, k, H, I = 32, 4, 2880, 2880 // tp
+    dev = "cuda"
+    g = torch.Generator(device=dev).manual_seed(0)
+    gu_b, gu_s = _quant_experts(torch.randn(E, 2 * I, H, device=dev, generator=g) * H ** -0.5)
+    dn_b, dn_s = _quant_experts(torch.randn(E, H, I, device=dev, generator=g) * I ** -0.5)
+    w_gu, w_dn = dequant_mxfp4(gu_b, gu_s), dequant_mxfp4(dn_b, dn_s)
+    fp4_gu, fp4_dn = M.pack_mxfp4(gu_b, gu_s), M.pack_mxfp4(dn_b, dn_s)
+    rw = (torch.randn(E, H, device=dev, generator=g) * 0.05).to(torch.bfloat16)
+    ws = M.MoEWorkspace.create(128, k, E, E, H, I, dev)
+    rows = []
+    for T in (1, 8, 32, 64, 128):
+        x = torch.randn(T, H, device=dev, generator=g).to(torch.bfloat16)
+        t_bf16 = timeit(lambda: M.moe_block(x, rw, w_gu, w_dn, k, M.ROUTE_TOPK_SOFTMAX, act=M.ACT_GPTOSS, ws=ws))
+        t_fp4 = timeit(lambda: M.moe_block(x, rw, w_gu, w_dn, k, M.ROUTE_TOPK_SOFTMAX, act=M.ACT_GPTOSS, ws=ws,
+                                           fp4_gu=fp4_gu, fp4_down=fp4_dn, fp4_max_tokens=1 << 20))
+        active = int(torch.unique(ws.ids[:T]).numel())
+        fp4_bytes = active * (fp4_gu[0].numel() + fp4_dn[0].numel())
+        bf16_bytes = active * (w_gu[0].numel() + w_dn[0].numel()) * 2
+        r = {"kernel": "moe_block_gptoss", "T": T, "tp": tp, "active_experts": active,
+             "bf16_us": t_bf16 * 1e3, "fp4_us": t_fp4 * 1e3,
+             "bf16_weight_GBs": bf16_bytes / (t_bf16 * 1e-3) / 1e9,
+             "fp4_weight_GBs": fp4_bytes / (t_fp4 * 1e-3) / 1e9}
+        print(json.dumps(r), flush=True)
+        rows.append(r)
+    return rows
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--tp", type=int, default=1)
     ap.add_argument("--json", type=str, default=None)
-    ap.add_argument("--only", type=str, default="gemm,decode,prefill")
+    ap.add_argument("--only", type=str, default="gemm,decode,prefill,moe")
     a = ap.parse_args()
     torch.manual_seed(0)
     rows = []
@@ -153,6 +186,8 @@ def main():
         rows += bench_decode_attention(a.tp)
     if "prefill" in only:
         rows += bench_prefill_attention(a.tp)
+    if "moe" in only:
+        rows += bench_moe(a.tp)
     if a.json:
         with open(a.json, "w") as f:
             json.dump(rows, f, indent=1)

@@ -580,22 +580,25 @@ void apply_token_bitmask(at::Tensor& logits, const at::Tensor& mask) {
   check_launch("apply_token_bitmask", logits.size(0) > 0 ? 1 : 0);
 }
 
-void moe_mxfp4_gemm(const at::Tensor& x, const at::Tensor& wq, const at::Tensor& ws, at::Tensor& out,
+// wt: MXFP4 weight tiles [E, ceil(N / 256), K / 64, tile_bytes] uint8 (ops.moe.pack_mxfp4);
+// N = out.size(1).
+void moe_mxfp4_gemm(const at::Tensor& x, const at::Tensor& wt, at::Tensor& out,
                     const at::Tensor& gtiles, const at::Tensor& gcount) {
   CHECK_CUDA(x);
   CHECK_BF16(x);
   CHECK_BF16(out);
-  TORCH_CHECK(wq.scalar_type() == at::kByte && ws.scalar_type() == at::kByte && wq.dim() == 3 &&
-                  ws.dim() == 3 && wq.is_contiguous() && ws.is_contiguous(),
-              "moe_mxfp4_gemm: wq [E, N, K/2] and ws [E, N, K/32] uint8");
-  const int K = (int)wq.size(2) * 2;
-  TORCH_CHECK(x.size(1) == K && ws.size(2) * 32 == K && out.size(1) == wq.size(1), "moe_mxfp4_gemm: shapes");
+  TORCH_CHECK(wt.scalar_type() == at::kByte && wt.dim() == 4 && wt.is_contiguous() &&
+                  wt.size(3) == b200::moe_mxfp4_tile_bytes(),
+              "moe_mxfp4_gemm: wt must be uint8 [E, N/256, K/64, tile_bytes]");
+  const int K = (int)wt.size(2) * 64;
+  const int N = (int)out.size(1);
+  TORCH_CHECK(x.size(1) == K && wt.size(1) * b200::moe_mxfp4_tile_cols() >= N, "moe_mxfp4_gemm: shapes");
   TORCH_CHECK(x.stride(1) == 1 && out.stride(1) == 1, "moe_mxfp4_gemm: layouts");
   const c10::cuda::CUDAGuard guard(x.device());
   b200::moe_mxfp4_gemm_launch(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0),
-                              wq.data_ptr<uint8_t>(), ws.data_ptr<uint8_t>(), gtiles.data_ptr<int>(),
-                              gcount.data_ptr<int>(), (int)gtiles.size(0), (int)wq.size(1), K,
-                              reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0), cur_stream());
+                              wt.data_ptr<uint8_t>(), gtiles.data_ptr<int>(), gcount.data_ptr<int>(),
+                              (int)gtiles.size(0), N, K, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+                              out.stride(0), status_word(), cur_stream());
   check_launch("moe_mxfp4_gemm");
 }
 

@@ -155,6 +155,17 @@ __device__ __forceinline__ void tma_load_2d(const void* desc, uint64_t* bar, voi
       : "memory");
 }
 
+// 1D bulk copy global -> this CTA's shared memory, completing on an mbarrier (16-byte aligned
+// addresses, size a multiple of 16).
+__device__ __forceinline__ void bulk_load_1d(void* smem_dst, const void* src, uint32_t bytes,
+                                             uint64_t* bar, uint64_t cache_hint) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(smem_dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(cache_hint)
+      : "memory");
+}
+
 // 3D tiled load (x innermost).
 __device__ __forceinline__ void tma_load_3d(const void* desc, uint64_t* bar, void* smem_dst,
                                             int32_t x, int32_t y, int32_t z,

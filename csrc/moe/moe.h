@@ -43,9 +43,11 @@ void moe_combine_launch(const __nv_bfloat16* y, const int* inv_pos, const float*
                         cudaStream_t s);
 
 // Y[rows, N] = X[rows, K] @ dequant(W_e)^T for the tile list of moe_align (<= 16 rows per pass),
-// W in MXFP4 repacked in fragment order (moe_mxfp4.cu): wq [E, N, K/2] uint8, ws [E, N, K/32].
-void moe_mxfp4_gemm_launch(const __nv_bfloat16* x, long long ldx, const uint8_t* wq,
-                           const uint8_t* ws, const int* gtiles, const int* gcount, int gmax, int N,
-                           int K, __nv_bfloat16* y, long long ldy, cudaStream_t s);
+// W in MXFP4 tiles (moe_mxfp4.cu): wt [E, ceil(N / 256), K / 64, tile_bytes] uint8.
+int moe_mxfp4_tile_bytes();
+int moe_mxfp4_tile_cols();
+void moe_mxfp4_gemm_launch(const __nv_bfloat16* x, long long ldx, const uint8_t* wt,
+                           const int* gtiles, const int* gcount, int gmax, int N, int K,
+                           __nv_bfloat16* y, long long ldy, uint32_t* status, cudaStream_t s);
 
 }  // namespace b200

@@ -73,26 +73,32 @@ def test_mxfp4_roundtrip_matches_transformers_dequant():
 
 
 def test_mxfp4_kernel_layout_roundtrip():
-    """Emulate the MXFP4 kernel's fragment reads (lane t, 64-k chunk c: bytes 8t..8t+7 of the
-    repacked row hold k = 16s + 2t, +1 (byte 2s) and 16s + 2t + 8, +9 (byte 2s + 1))."""
+    """Emulate the MXFP4 kernel's reads of its weight tiles (tile (nb, c): column r's 32 bytes at
+    r * 32, lane t's 8 bytes at 8t: byte 2s holds k = 16s + 2t, +1, byte 2s + 1 holds
+    k = 16s + 2t + 8, +9; scales at 256 * 32 + 2r)."""
     from vllm_neuron_b200.models.gpt_oss import _FP4_VALUES, dequant_mxfp4, quant_mxfp4
-    from vllm_neuron_b200.ops.moe import pack_mxfp4
+    from vllm_neuron_b200.ops.moe import TILE_COLS, pack_mxfp4
 
-    w = torch.randn(2, 5, 128) * 0.3
+    E, N, K = 2, 300, 128
+    w = torch.randn(E, N, K) * 0.3
     blocks, scales = quant_mxfp4(w)
     ref = dequant_mxfp4(blocks, scales, torch.float32)
-    wq, ws = pack_mxfp4(blocks, scales)
+    wt = pack_mxfp4(blocks, scales)
+    assert wt.shape == (E, 2, K // 64, TILE_COLS * 34)
     lut = torch.tensor(_FP4_VALUES)
     got = torch.zeros_like(ref)
-    for e in range(2):
-        for n in range(5):
-            for c in range(2):
+    for e in range(E):
+        for n in range(N):
+            nb, r = divmod(n, TILE_COLS)
+            for c in range(K // 64):
+                tile = wt[e, nb, c]
+                sc = tile[TILE_COLS * 32 + 2 * r:TILE_COLS * 32 + 2 * r + 2].tolist()
                 for t in range(4):
-                    by = wq[e, n, c * 32 + 8 * t:c * 32 + 8 * t + 8].tolist()
+                    by = tile[r * 32 + 8 * t:r * 32 + 8 * t + 8].tolist()
                     for s in range(4):
-                        sc = 2.0 ** (int(ws[e, n, 2 * c + s // 2]) - 127)
+                        f = 2.0 ** (sc[s // 2] - 127)
                         for half, b in enumerate((by[2 * s], by[2 * s + 1])):
                             k = c * 64 + 16 * s + 2 * t + 8 * half
-                            got[e, n, k] = lut[b & 15] * sc
-                            got[e, n, k + 1] = lut[b >> 4] * sc
+                            got[e, n, k] = lut[b & 15] * f
+                            got[e, n, k + 1] = lut[b >> 4] * f
     assert torch.equal(got, ref)

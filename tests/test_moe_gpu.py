@@ -104,8 +104,8 @@ def test_moe_block_mxfp4_decode(cuda_device, T):
     dn_b, dn_s = quant_mxfp4(torch.randn(E, H, I, generator=torch.Generator().manual_seed(5)) * I ** -0.5)
     w_gu = dequant_mxfp4(gu_b, gu_s).to(cuda_device)
     w_dn = dequant_mxfp4(dn_b, dn_s).to(cuda_device)
-    fp4_gu = tuple(t.to(cuda_device) for t in M.pack_mxfp4(gu_b, gu_s))
-    fp4_dn = tuple(t.to(cuda_device) for t in M.pack_mxfp4(dn_b, dn_s))
+    fp4_gu = M.pack_mxfp4(gu_b, gu_s).to(cuda_device)
+    fp4_dn = M.pack_mxfp4(dn_b, dn_s).to(cuda_device)
     ws = M.MoEWorkspace.create(64, k, E, E, H, I, cuda_device)
     out = M.moe_block(x, rw, w_gu, w_dn, k, M.ROUTE_TOPK_SOFTMAX, act=M.ACT_GPTOSS, ws=ws,
                       fp4_gu=fp4_gu, fp4_down=fp4_dn)

@@ -112,8 +112,8 @@ class GptOssForCausalLM(LlamaForCausalLM):
             dn_blocks, dn_scales = _quant_experts(ly.w_down)
         ly.w_gu.copy_(dequant_mxfp4(gu_blocks, gu_scales).to(ly.w_gu.device))
         ly.w_down.copy_(dequant_mxfp4(dn_blocks, dn_scales).to(ly.w_down.device))
-        ly.fp4_gu = tuple(t.to(self.device) for t in M.pack_mxfp4(gu_blocks, gu_scales))
-        ly.fp4_down = tuple(t.to(self.device) for t in M.pack_mxfp4(dn_blocks, dn_scales))
+        ly.fp4_gu = M.pack_mxfp4(gu_blocks.to(self.device), gu_scales.to(self.device))
+        ly.fp4_down = M.pack_mxfp4(dn_blocks.to(self.device), dn_scales.to(self.device))
 
     def _mlp(self, i, ly, x, res, nxt_norm, T, small, fused):
         h = self.ws_h[:T]

@@ -164,17 +164,28 @@ def route(logits: torch.Tensor, k: int, mode: int, renorm: bool = True,
     return ids, weights
 
 
-def pack_mxfp4(blocks: torch.Tensor, scales: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-    """Checkpoint MXFP4 ``blocks [..., N, K/32, 16]`` / ``scales [..., N, K/32]`` -> the kernel
-    layout ``wq [..., N, K/2]`` (inside every 32-byte group, byte ``8t + j`` = original byte
-    ``t + 4j``: the order lane t of an m16n8k16 B fragment consumes) and ``ws [..., N, K/32]``."""
-    *lead, N, G, _ = blocks.shape
-    b = blocks.reshape(*lead, N, G * 16)
-    K2 = G * 16
-    assert K2 % 32 == 0, "K must be a multiple of 64"
-    v = b.reshape(*lead, N, K2 // 32, 8, 4)            # [.., chunk, j, t] = byte t + 4j
-    wq = v.transpose(-1, -2).reshape(*lead, N, K2)     # [.., chunk, t, j] -> byte 8t + j
-    return wq.contiguous(), scales.reshape(*lead, N, G).contiguous()
+TILE_COLS = 256
+
+
+def pack_mxfp4(blocks: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+    """Checkpoint MXFP4 ``blocks [E, N, K/32, 16]`` / ``scales [E, N, K/32]`` -> the kernel's
+    weight tiles ``[E, ceil(N/256), K/64, 256*32 + 256*2]`` uint8 (csrc/moe/moe_mxfp4.cu):
+    per tile the 256 columns' 32 bytes of a 64-k chunk, each 32-byte group reordered so byte
+    ``8t + j`` = original byte ``t + 4j`` (the order lane t of an m16n8k16 B fragment
+    consumes), followed by the columns' two e8m0 scales."""
+    E, N, G, _ = blocks.shape
+    assert G % 2 == 0, "K must be a multiple of 64"
+    KC = G // 2
+    NB = -(-N // TILE_COLS)
+    b = blocks.reshape(E, N, KC, 8, 4).transpose(-1, -2).reshape(E, N, KC, 32)  # fragment order
+    sc = scales.reshape(E, N, KC, 2)
+    pad = NB * TILE_COLS - N
+    if pad:
+        b = torch.cat([b, torch.zeros(E, pad, KC, 32, dtype=b.dtype, device=b.device)], 1)
+        sc = torch.cat([sc, torch.zeros(E, pad, KC, 2, dtype=sc.dtype, device=sc.device)], 1)
+    b = b.view(E, NB, TILE_COLS, KC, 32).permute(0, 1, 3, 2, 4).reshape(E, NB, KC, TILE_COLS * 32)
+    sc = sc.view(E, NB, TILE_COLS, KC, 2).permute(0, 1, 3, 2, 4).reshape(E, NB, KC, TILE_COLS * 2)
+    return torch.cat([b, sc], -1).contiguous()
 
 
 def mxfp4_gemm_ref(x: torch.Tensor, rows_expert: torch.Tensor, w_bf16: torch.Tensor) -> torch.Tensor:
@@ -194,8 +205,8 @@ def moe_block(x: torch.Tensor, router_w: torch.Tensor, w_gu: torch.Tensor, w_dow
               act: int = ACT_SILU, alpha: float = 1.702, limit: float = 7.0, e_start: int = 0,
               ws: MoEWorkspace | None = None, out: torch.Tensor | None = None,
               num_experts: int | None = None, shared_gu: torch.Tensor | None = None,
-              shared_down: torch.Tensor | None = None, fp4_gu: tuple | None = None,
-              fp4_down: tuple | None = None, fp4_max_tokens: int = 64) -> torch.Tensor:
+              shared_down: torch.Tensor | None = None, fp4_gu: torch.Tensor | None = None,
+              fp4_down: torch.Tensor | None = None, fp4_max_tokens: int = 64) -> torch.Tensor:
     """Routed experts for ``x [T, H]`` (see the module docstring); returns ``out [T, H]`` bf16.
 
     ``w_gu [e_local, 2I, H]`` holds each expert's gate rows followed by its up rows,
@@ -248,14 +259,14 @@ def moe_block(x: torch.Tensor, router_w: torch.Tensor, w_gu: torch.Tensor, w_dow
     # every tile-list entry holds >= 1 row: at most R entries exist (bounds the fp4 grid)
     gt = ws.gtiles[:min(ws.gtiles.shape[0], R)]
     if use_fp4:
-        ext().moe_mxfp4_gemm(xp, fp4_gu[0], fp4_gu[1], gu, gt, ws.gcount)
+        ext().moe_mxfp4_gemm(xp, fp4_gu, gu, gt, ws.gcount)
     else:
         ext().gemm_grouped(xp, w_gu, gu, ws.gtiles, ws.gcount, EPI_BF16, 256)
     a = ws.act[:R, :I]
     ext().moe_act(gu, b_gu, ws.row_expert, ws.offsets, act, alpha, limit, a)
     y = ws.y[:R]
     if use_fp4:
-        ext().moe_mxfp4_gemm(a, fp4_down[0], fp4_down[1], y, gt, ws.gcount)
+        ext().moe_mxfp4_gemm(a, fp4_down, y, gt, ws.gcount)
     else:
         ext().gemm_grouped(a, w_down, y, ws.gtiles, ws.gcount, EPI_BF16, 256 if H % 256 == 0 else 128)
     ext().moe_combine(y, ws.inv_pos[:R], w, ids, b_down, e_start, shared,
