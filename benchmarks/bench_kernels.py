@@ -140,7 +140,9 @@ def bench_prefill_attention(tp: int):
 
 def bench_moe(tp: int):
     """GPT-OSS-20B expert block (32 experts top-4, hidden 2880, FFN 2880) at decode batch sizes:
-    bf16 grouped tcgen05 GEMMs against the MXFP4 decode kernel (same routing, same weights)."""
+    bf16 grouped tcgen05 GEMMs against the MXFP4 decode kernel (same routing, same weights),
+    each block replayed from a CUDA graph.  The weight bandwidth counts only the active experts'
+    weight bytes (router, routing and combine time included in the denominator)."""
     from vllm_neuron_b200.models.gpt_oss import _quant_experts, dequant_mxfp4
     from vllm_neuron_b200.ops import moe as M
 
@@ -156,9 +158,20 @@ def bench_moe(tp: int):
     rows = []
     for T in (1, 8, 32, 64, 128):
         x = torch.randn(T, H, device=dev, generator=g).to(torch.bfloat16)
-        t_bf16 = timeit(lambda: M.moe_block(x, rw, w_gu, w_dn, k, M.ROUTE_TOPK_SOFTMAX, act=M.ACT_GPTOSS, ws=ws))
-        t_fp4 = timeit(lambda: M.moe_block(x, rw, w_gu, w_dn, k, M.ROUTE_TOPK_SOFTMAX, act=M.ACT_GPTOSS, ws=ws,
-                                           fp4_gu=fp4_gu, fp4_down=fp4_dn, fp4_max_tokens=1 << 20))
+
+        def graph(fp4: bool):
+            kw = dict(fp4_gu=fp4_gu, fp4_down=fp4_dn, fp4_max_tokens=1 << 20) if fp4 else {}
+            run = lambda: M.moe_block(x, rw, w_gu, w_dn, k, M.ROUTE_TOPK_SOFTMAX, act=M.ACT_GPTOSS, ws=ws, **kw)
+            run()  # compile-time setup (shared-memory opt-in) outside the capture
+            torch.cuda.synchronize()
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                run()
+            return gr.replay
+
+        # decode replays the block from a CUDA graph; time it the same way (no host gaps)
+        t_bf16 = timeit(graph(False))
+        t_fp4 = timeit(graph(True))
         active = int(torch.unique(ws.ids[:T]).numel())
         fp4_bytes = active * (fp4_gu[0].numel() + fp4_dn[0].numel())
         bf16_bytes = active * (w_gu[0].numel() + w_dn[0].numel()) * 2

@@ -34,7 +34,7 @@ def main():
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--ctx", type=int, default=1152)
     ap.add_argument("--chunk", type=int, default=8192)
-    ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--layers", type=int, default=None, help="default: the model's layer count")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--json", type=str, default=None)
     ap.add_argument("--no-fused", action="store_true", help="TP: NCCL all-reduce instead of the fused kernel")
@@ -49,6 +49,7 @@ def main():
     rank, world = ps.init_distributed(timeout_s=300)
     if world > 1:
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    a.layers = min(a.layers or MODELS[a.model]["cfg"]["num_hidden_layers"], MODELS[a.model]["cfg"]["num_hidden_layers"])
     cfg = dict(MODELS[a.model]["cfg"], num_hidden_layers=a.layers)
     if "layer_types" in cfg:
         cfg["layer_types"] = cfg["layer_types"][:a.layers]
