@@ -253,10 +253,13 @@ def main():
             "fused_tp_comm": eng.model.tp_fused is not None,
         }
         print(json.dumps(line), flush=True)
-    llm.shutdown()
     if world > 1:
+        # Every rank has finished its collectives; leave without tearing down the process group
+        # (graph-held communicators otherwise make the exit wait).
         dist.barrier()
-        dist.destroy_process_group()
+        sys.stdout.flush()
+        os._exit(0)
+    llm.shutdown()
 
 
 if __name__ == "__main__":

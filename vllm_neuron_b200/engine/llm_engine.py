@@ -13,7 +13,9 @@ from dataclasses import dataclass, field
 import numpy as np
 import torch
 
+from .. import envs
 from ..config import B200Config, ModelArchConfig
+from ..exceptions import DeviceStatusError
 from ..metrics import Metrics
 from ..parallel.comm import SINGLE, GroupComm
 from .block_manager import BlockManager
@@ -94,7 +96,8 @@ class LLMEngine:
         else:
             load_checkpoint_into(self.model, self.model_path)
         real_group = tp.world > 1 and tp.group is not None
-        if real_group and self.device.type == "cuda" and self.b200_config.fused_comm:
+        if (real_group and self.device.type == "cuda" and self.b200_config.fused_comm
+                and not envs.VLLM_B200_DISABLE_FUSED_COMM):
             from ..parallel import state as ps
 
             self.model.enable_fused_comm(ps.get_parallel_state().cpu)
@@ -178,8 +181,7 @@ class LLMEngine:
 
         code = int(ext().read_status())
         if code != 0:
-            raise RuntimeError(f"device status {code}: a bounded wait of a fused collective expired "
-                               "(a peer rank stopped or fell out of step)")
+            raise DeviceStatusError(code, f"engine step {self.num_steps}")
 
     @torch.no_grad()
     def prompt_hidden(self, prompts: list[list[int]]) -> torch.Tensor:
@@ -218,7 +220,10 @@ class LLMEngine:
     # ---------------------------------------------------------------- stepping
     def _process(self, out, handle) -> list[Request]:
         toks, lps = handle.result()
-        if getattr(self.model, "tp_fused", None) is not None and self.num_steps % 16 == 0:
+        if envs.VLLM_B200_DEBUG_MODE and self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+            self._check_device_status()
+        elif getattr(self.model, "tp_fused", None) is not None and self.num_steps % 16 == 0:
             self._check_device_status()
         now = time.perf_counter()
         finished = self.scheduler.update(out, toks, lps, now=now)
@@ -244,7 +249,7 @@ class LLMEngine:
 
         from torch.profiler import ProfilerActivity, profile
 
-        self._profile_dir = out_dir or os.environ.get("VLLM_B200_PROFILE_DIR", "b200_profile")
+        self._profile_dir = out_dir or envs.VLLM_B200_PROFILE_DIR
         acts = [ProfilerActivity.CPU] + ([ProfilerActivity.CUDA] if self.device.type == "cuda" else [])
         self._profiler = profile(activities=acts, record_shapes=False)
         self._profiler.__enter__()

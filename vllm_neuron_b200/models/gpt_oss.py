@@ -18,7 +18,7 @@ from __future__ import annotations
 
 import torch
 
-from .. import ops
+from .. import envs, ops
 from ..ops import moe as M
 from .llama import LlamaForCausalLM
 
@@ -88,6 +88,7 @@ class GptOssForCausalLM(LlamaForCausalLM):
         # MXFP4 copies of the experts for decode-sized batches (K = H for gate/up, I for down
         # must be multiples of 64); the bf16 copies serve prefill.
         self.use_fp4 = self.device.type == "cuda" and self.H % 64 == 0 and self.I_moe % 64 == 0
+        self.fp4_max_tokens = envs.VLLM_B200_FP4_DECODE_MAX_TOKENS
         for ly in self.layers:
             ly.fp4_gu = ly.fp4_down = None
 
@@ -122,7 +123,7 @@ class GptOssForCausalLM(LlamaForCausalLM):
                     b_down=ly.b_down,  # each assignment is computed on exactly one rank
                     act=M.ACT_GPTOSS, alpha=self.cfg.swiglu_alpha, limit=self.cfg.swiglu_limit,
                     e_start=self.e_start, ws=self.moe_ws, out=h, fp4_gu=ly.fp4_gu,
-                    fp4_down=ly.fp4_down)
+                    fp4_down=ly.fp4_down, fp4_max_tokens=self.fp4_max_tokens)
         self.tp.all_reduce_(h)
         ops.add_rmsnorm(h, res, nxt_norm, self.eps, out=x)
 

@@ -171,12 +171,15 @@ def get_parallel_state() -> ParallelState:
     return _STATE
 
 
-def world_barrier(timeout_s: float = 3600.0):
+def world_barrier(timeout_s: float | None = None):
     """Barrier over the gloo CPU group with a timeout (reference: world_barrier,
     neuron_parallel_state.py:1568-1604; timeout from VLLM_NEURON_BARRIER_TIMEOUT)."""
     st = get_parallel_state()
     if st.cpu is None:
         return
+    from .. import envs
+
+    timeout_s = timeout_s if timeout_s is not None else envs.VLLM_B200_BARRIER_TIMEOUT
     st.cpu.barrier().wait(datetime.timedelta(seconds=timeout_s))
 
 

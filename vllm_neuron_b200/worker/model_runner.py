@@ -20,7 +20,8 @@ from dataclasses import dataclass
 import numpy as np
 import torch
 
-from .. import ops
+from .. import envs, ops
+from ..exceptions import KVCacheBudgetError
 from ..engine.scheduler import SchedulerOutput
 from ..models.llama import ForwardBatch
 
@@ -66,7 +67,7 @@ class ModelRunner:
         self.max_model_len = max_model_len
         self.block_size = block_size
         self.max_blocks = (max_model_len + block_size - 1) // block_size
-        self.use_graphs = cuda_graphs and self.is_cuda
+        self.use_graphs = cuda_graphs and self.is_cuda and not envs.VLLM_B200_DISABLE_CUDA_GRAPHS
         cap = min(max_num_seqs, model.max_decode_tokens)
         self.graph_buckets = sorted(b for b in (graph_buckets or [1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128])
                                     if b <= cap)
@@ -106,8 +107,8 @@ class ModelRunner:
         # directory (reference: vllm_neuron/snapshot/*, runtime input capture).
         import os
 
-        self.snapshot_dir = os.environ.get("VLLM_B200_SNAPSHOT_DIR") or None
-        self.snapshot_max = int(os.environ.get("VLLM_B200_SNAPSHOT_MAX_STEPS", "64"))
+        self.snapshot_dir = envs.VLLM_B200_SNAPSHOT_DIR
+        self.snapshot_max = envs.VLLM_B200_SNAPSHOT_MAX_STEPS
         self._snap_n = 0
 
     def _max_work(self) -> int:
@@ -135,9 +136,15 @@ class ModelRunner:
         free, total = torch.cuda.mem_get_info(self.device)
         used = total - free
         budget = total * gpu_memory_utilization - used - reserve_bytes
+        cap = envs.VLLM_B200_KV_CACHE_MAX_GIB
+        if cap is not None:
+            budget = min(budget, cap * 2**30)
+        if budget < (envs.VLLM_B200_MIN_KV_BUDGET_GIB or 0.0) * 2**30:
+            raise KVCacheBudgetError(f"KV-cache budget {budget / 2**30:.2f} GiB is below "
+                                     f"VLLM_B200_MIN_KV_BUDGET_GIB={envs.VLLM_B200_MIN_KV_BUDGET_GIB}")
         n = int(budget // self.kv_bytes_per_block())
         if n < 2:
-            raise RuntimeError(f"not enough memory for the KV cache (budget {budget / 2**30:.2f} GiB)")
+            raise KVCacheBudgetError(f"not enough memory for the KV cache (budget {budget / 2**30:.2f} GiB)")
         return n
 
     # ------------------------------------------------------------------ input packing
