@@ -7,7 +7,7 @@ source tree.
 import glob
 import os
 
-from setuptools import setup
+from setuptools import find_packages, setup
 from torch.utils.cpp_extension import BuildExtension, CUDAExtension
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -31,7 +31,10 @@ def sources():
 setup(
     name="vllm_neuron_b200",
     version="0.1.0",
-    packages=[],
+    packages=find_packages(include=["vllm_neuron_b200", "vllm_neuron_b200.*"]),
+    # vLLM discovers the B200 platform through this plugin group once the package is installed
+    # (pip install -e .): `vllm serve` / vllm.LLM then run on this framework's worker.
+    entry_points={"vllm.platform_plugins": ["b200 = vllm_neuron_b200.vllm_plugin:register"]},
     ext_modules=[
         CUDAExtension(
             name="vllm_neuron_b200._C",

@@ -65,48 +65,64 @@ class RequestOutput:
     metrics: dict = field(default_factory=dict)
 
 
+def build_model(args: EngineArgs, tp: GroupComm = SINGLE):
+    """Resolve the architecture of ``args.model`` (HF config dict, ModelArchConfig or a
+    checkpoint directory), build the model for this TP rank and load (or random-init) its
+    weights.  Returns ``(arch, model, model_path, device, b200_config)``."""
+    from ..models import registry
+    from ..utils.checkpoints import load_checkpoint_into
+
+    b200_config = B200Config.from_additional_config(args.additional_config)
+    model_path = None
+    if isinstance(args.model, dict):
+        arch = ModelArchConfig.from_hf(args.model)
+    elif isinstance(args.model, ModelArchConfig):
+        arch = args.model
+    else:
+        model_path = args.model
+        arch = ModelArchConfig.from_path(args.model)
+    device = torch.device(args.device)
+    if device.type == "cuda" and device.index is None:
+        device = torch.device("cuda", torch.cuda.current_device())
+    dtype = {"bfloat16": torch.bfloat16, "float32": torch.float32, "float16": torch.float16}[args.dtype]
+    cls = registry.resolve(arch.architectures)
+    max_tok = max(args.max_num_batched_tokens, args.max_num_seqs)
+    model = cls(arch, tp=tp, device=device, dtype=dtype, max_tokens=max_tok,
+                max_seqs=args.max_num_seqs, block_size=args.block_size)
+    if args.load_format == "dummy" or model_path is None:
+        model.init_random(seed=args.seed)
+    else:
+        load_checkpoint_into(model, model_path)
+    real_group = tp.world > 1 and tp.group is not None
+    if (real_group and device.type == "cuda" and b200_config.fused_comm
+            and not envs.VLLM_B200_DISABLE_FUSED_COMM):
+        from ..parallel import state as ps
+
+        model.enable_fused_comm(ps.get_parallel_state().cpu)
+    return arch, model, model_path, device, b200_config
+
+
+def build_runner(args: EngineArgs, model, max_model_len: int, device, b200_config):
+    """The model runner of ``model`` (KV cache not yet allocated)."""
+    from ..worker.model_runner import ModelRunner
+
+    return ModelRunner(model, max_num_seqs=args.max_num_seqs,
+                       max_num_batched_tokens=max(args.max_num_batched_tokens, args.max_num_seqs),
+                       max_model_len=max_model_len, block_size=args.block_size,
+                       cuda_graphs=(args.cuda_graphs and b200_config.cuda_graphs
+                                    and getattr(model, "supports_cuda_graphs", True)),
+                       device=device, seed=args.seed)
+
+
 class LLMEngine:
     def __init__(self, args: EngineArgs, tp: GroupComm = SINGLE):
-        from ..models import registry
-        from ..utils.checkpoints import load_checkpoint_into
-        from ..worker.model_runner import ModelRunner
-
         self.args = args
         self.tp = tp
-        self.b200_config = B200Config.from_additional_config(args.additional_config)
-        self.model_path = None
-        if isinstance(args.model, dict):
-            self.arch = ModelArchConfig.from_hf(args.model)
-        elif isinstance(args.model, ModelArchConfig):
-            self.arch = args.model
-        else:
-            self.model_path = args.model
-            self.arch = ModelArchConfig.from_path(args.model)
+        self.arch, self.model, self.model_path, self.device, self.b200_config = build_model(args, tp)
         self.max_model_len = args.max_model_len or self.arch.max_position_embeddings
-        self.device = torch.device(args.device)
-        if self.device.type == "cuda" and self.device.index is None:
-            self.device = torch.device("cuda", torch.cuda.current_device())
-        dtype = {"bfloat16": torch.bfloat16, "float32": torch.float32, "float16": torch.float16}[args.dtype]
-        cls = registry.resolve(self.arch.architectures)
         max_tok = max(args.max_num_batched_tokens, args.max_num_seqs)
-        self.model = cls(self.arch, tp=tp, device=self.device, dtype=dtype, max_tokens=max_tok,
-                         max_seqs=args.max_num_seqs, block_size=args.block_size)
-        if args.load_format == "dummy" or self.model_path is None:
-            self.model.init_random(seed=args.seed)
-        else:
-            load_checkpoint_into(self.model, self.model_path)
         real_group = tp.world > 1 and tp.group is not None
-        if (real_group and self.device.type == "cuda" and self.b200_config.fused_comm
-                and not envs.VLLM_B200_DISABLE_FUSED_COMM):
-            from ..parallel import state as ps
-
-            self.model.enable_fused_comm(ps.get_parallel_state().cpu)
-        self.runner = ModelRunner(self.model, max_num_seqs=args.max_num_seqs,
-                                  max_num_batched_tokens=max_tok, max_model_len=self.max_model_len,
-                                  block_size=args.block_size,
-                                  cuda_graphs=(args.cuda_graphs and self.b200_config.cuda_graphs
-                                               and getattr(self.model, "supports_cuda_graphs", True)),
-                                  device=self.device, seed=args.seed)
+        self.runner = build_runner(args, self.model, self.max_model_len, self.device, self.b200_config)
         nb = args.num_gpu_blocks or self.runner.profile_num_blocks(args.gpu_memory_utilization)
         if real_group and self.device.type == "cuda":
             t = torch.tensor([nb], dtype=torch.int64, device=self.device)
