@@ -39,7 +39,7 @@ def test_vllm_engine_on_b200(tmp_path):
                             SamplingParams(max_tokens=24, temperature=0.0, ignore_eos=True))
         got = [list(o.outputs[0].token_ids) for o in outs]
         launched = ext().launch_count() - n0
-        worker = llm.llm_engine.model_executor.driver_worker.worker
+        worker = llm.llm_engine.engine_core.engine_core.model_executor.driver_worker.worker
         replays = worker.runner.num_graph_replays
         del llm
         from vllm_neuron_b200.engine.sampling_params import SamplingParams as SP
