@@ -16,7 +16,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, ckpt, prompts, q, tp=None):
+def _worker(rank, world, port, ckpt, prompts, q, tp=None, extra=None):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
                       WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
     import torch
@@ -28,9 +28,10 @@ def _worker(rank, world, port, ckpt, prompts, q, tp=None):
 
     try:
         llm = LLM(ckpt, tensor_parallel_size=tp or world, device="cpu", max_num_seqs=8, max_model_len=128,
-                  num_gpu_blocks=64, max_num_batched_tokens=48)
+                  num_gpu_blocks=64, **dict(dict(max_num_batched_tokens=48), **(extra or {})))
         outs = llm.generate(prompts, SamplingParams(temperature=0, max_tokens=8, ignore_eos=True))
-        q.put((rank, [o.outputs[0].token_ids for o in outs]))
+        toks = [o.outputs[0].token_ids for o in outs]
+        q.put((rank, (toks, llm.engine.model.sp_forwards) if extra else toks))
     except Exception as e:  # pragma: no cover - reported to the parent
         q.put((rank, repr(e)))
     finally:
@@ -57,6 +58,33 @@ def test_tp2_matches_tp1():
         p.join(timeout=60)
     assert res[0] == ref, res[0]
     assert res[1] == ref, res[1]
+
+
+def test_tp2_sequence_parallel_matches_tp1():
+    """Prefill with the residual stream sharded over tokens (reduce-scatter / all-gather, odd
+    token counts padded to the TP size) gives the TP=1 tokens."""
+    ckpt, _ = tiny_llama_checkpoint()
+    prompts = random_prompts(n=3, length=71, seed=5)  # one 213-token prefill step (> decode path)
+    from vllm_neuron_b200.engine.sampling_params import SamplingParams
+    from vllm_neuron_b200.entrypoints import LLM
+
+    ref = LLM(ckpt, device="cpu", max_num_seqs=8, max_model_len=128, num_gpu_blocks=64,
+              max_num_batched_tokens=256).generate(prompts, SamplingParams(temperature=0, max_tokens=8, ignore_eos=True))
+    ref = [o.outputs[0].token_ids for o in ref]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    extra = {"additional_config": {"neuron_config": {"sequence_parallel": True}}, "max_num_batched_tokens": 256}
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, ckpt, prompts, q, None, extra)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    for r in (0, 1):
+        toks, n_sp = res[r]
+        assert toks == ref, toks
+        assert n_sp >= 1
 
 
 def test_dp2_matches_single_replica():

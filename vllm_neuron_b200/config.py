@@ -184,6 +184,7 @@ class B200Config:
     enable_structured_outputs: bool = True
     fp8_packed_kv: bool = False
     # B200-specific knobs
+    sequence_parallel: bool = False   # prefill: reduce-scatter / all-gather instead of all-reduce
     cuda_graphs: bool = True
     fused_comm: bool = True           # fused GEMM+collective kernels (else NCCL baseline)
     use_cublas_baseline: bool = False  # library GEMMs instead of the tcgen05 kernels

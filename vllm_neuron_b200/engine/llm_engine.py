@@ -94,6 +94,8 @@ def build_model(args: EngineArgs, tp: GroupComm = SINGLE):
     else:
         load_checkpoint_into(model, model_path)
     real_group = tp.world > 1 and tp.group is not None
+    if b200_config.sequence_parallel and hasattr(model, "sequence_parallel"):
+        model.sequence_parallel = True
     if (real_group and device.type == "cuda" and b200_config.fused_comm
             and not envs.VLLM_B200_DISABLE_FUSED_COMM):
         from ..parallel import state as ps

@@ -83,7 +83,7 @@ class GptOssForCausalLM(LlamaForCausalLM):
                                           requires_grad=False)
         self.moe_ws = None
         if self.device.type == "cuda":
-            self.moe_ws = M.MoEWorkspace.create(self.max_tokens, self.topk, self.E, self.e_local, self.H,
+            self.moe_ws = M.MoEWorkspace.create(self.max_tokens + self.tp.world, self.topk, self.E, self.e_local, self.H,
                                                 self.I_moe, self.device)
         # MXFP4 copies of the experts for decode-sized batches (K = H for gate/up, I for down
         # must be multiples of 64); the bf16 copies serve prefill.
@@ -124,8 +124,7 @@ class GptOssForCausalLM(LlamaForCausalLM):
                     act=M.ACT_GPTOSS, alpha=self.cfg.swiglu_alpha, limit=self.cfg.swiglu_limit,
                     e_start=self.e_start, ws=self.moe_ws, out=h, fp4_gu=ly.fp4_gu,
                     fp4_down=ly.fp4_down, fp4_max_tokens=self.fp4_max_tokens)
-        self.tp.all_reduce_(h)
-        ops.add_rmsnorm(h, res, nxt_norm, self.eps, out=x)
+        self._reduce_norm(h, res, nxt_norm, x)
 
     @torch.no_grad()
     def init_random(self, seed: int = 0, std: float = 0.02):

@@ -111,6 +111,9 @@ class LlamaForCausalLM(torch.nn.Module):
         self.kv_caches: list[tuple[torch.Tensor, torch.Tensor]] = []
         self._alloc_workspace(max_tokens, max_decode_tokens, max_seqs)
         self.tp_fused = None  # TPFusedComm: fused all-reduce + residual + RMSNorm (decode)
+        self.sequence_parallel = False  # prefill residual stream sharded over tokens (TP > 1)
+        self._sp = None                 # (padded tokens, local tokens) of the running SP forward
+        self.sp_forwards = 0            # forwards that ran sequence-parallel
         # Hidden states captured after these layers (EAGLE3 drafting): [tokens, len * H]
         self.aux_layers: list[int] = []
         self.aux_hidden: torch.Tensor | None = None
@@ -138,6 +141,11 @@ class LlamaForCausalLM(torch.nn.Module):
 
     def _alloc_workspace(self, max_tokens, max_dec, max_seqs):
         d, bf = self.device, self.dtype
+        W = self.tp.world
+        max_tokens = -(-max_tokens // W) * W  # sequence parallelism pads the tokens to W
+        # sequence-parallel local slices (residual stream sharded over tokens)
+        self.ws_sp_x = torch.zeros(max_tokens // W, self.H, dtype=bf, device=d)
+        self.ws_sp_h = torch.zeros(max_tokens // W, self.H, dtype=bf, device=d)
         self.ws_residual = torch.zeros(max_tokens, self.H, dtype=bf, device=d)
         self.ws_x = torch.zeros(max_tokens, self.H, dtype=bf, device=d)
         self.ws_qkv = torch.zeros(max_tokens, self.qkv_out, dtype=bf, device=d)
@@ -201,14 +209,7 @@ class LlamaForCausalLM(torch.nn.Module):
         small = T <= self.max_decode_tokens
         fused = small and self.tp_fused is not None
         tp = self.tp
-        res = self.ws_residual[:T]
-        x = self.ws_x[:T]
-        ops.embedding(b.input_ids, self.embed, self.vocab_start, self.vocab_start + self.V_local, out=res,
-                      last_tok=b.last_tok)
-        tp.all_reduce_(res)
-        if b.embed_rows is not None:
-            res.index_copy_(0, b.embed_rows, b.embeds.to(res.dtype))
-        ops.rmsnorm(res, self.layers[0].input_norm, self.eps, out=x)
+        res, x, Tg = self._embed(b, T, small)
         nL = len(self.layers)
         for i, ly in enumerate(self.layers):
             k_cache, v_cache = self.kv_caches[i]
@@ -223,7 +224,7 @@ class LlamaForCausalLM(torch.nn.Module):
                                   k_cache, v_cache, b.slot_mapping, ly.q_norm, ly.k_norm, self.eps,
                                   rot_dim=self.cfg.rot_dim, clear_input=True)
             else:
-                qkv = L.gemm_out(x, ly.qkv, out=self.ws_qkv[:T])
+                qkv = L.gemm_out(x[:T], ly.qkv, out=self.ws_qkv[:T])
                 if ly.qkv_bias is not None:
                     qkv.add_(ly.qkv_bias)
                 ops.rope_kv_write(qkv, b.positions, self.cos_sin, self.Hq, self.Hkv, self.D, q,
@@ -239,20 +240,78 @@ class LlamaForCausalLM(torch.nn.Module):
                     acc.add_(ly.o_bias.float())
                 self._allreduce_norm(acc, res, nxt_norm, x, fused)
             else:
-                h = L.gemm_out(attn, ly.o, out=self.ws_h[:T])
+                if Tg > T:
+                    self.ws_attn[T:Tg].zero_()
+                h = L.gemm_out(self.ws_attn[:Tg], ly.o, out=self.ws_h[:Tg])
                 if ly.o_bias is not None and tp.rank == 0:
                     h.add_(ly.o_bias)
-                tp.all_reduce_(h)
-                ops.add_rmsnorm(h, res, nxt_norm, self.eps, out=x)
+                self._reduce_norm(h, res, nxt_norm, x)
             # ---- MLP
             nxt_norm = self.layers[i + 1].input_norm if i + 1 < nL else self.final_norm
-            self._mlp(i, ly, x, res, nxt_norm, T, small, fused)
+            self._mlp(i, ly, x, res, nxt_norm, Tg, small, fused)
             if self.aux_layers and i in self.aux_layers:
                 j = self.aux_layers.index(i)
                 self.aux_hidden[:T, j * self.H:(j + 1) * self.H].copy_(res)
+        self._sp = None
         if b.want_hidden:
             return x.index_select(0, b.logits_indices.long())
         return self.compute_logits(x, b.logits_indices)
+
+    def _embed(self, b: ForwardBatch, T: int, small: bool):
+        """Embedding (vocab-parallel) and the first RMSNorm.  Returns ``(res, x, Tg)``: the
+        residual stream, the normalized full-token activations and the GEMM row count.
+
+        Under sequence parallelism (TP > 1 prefill) the token count is padded to a multiple of
+        the TP size ``Tg``; each rank keeps the residual rows ``[rank*Tg/W, (rank+1)*Tg/W)``
+        (reduce-scatter of the embedding partial sums) and ``x`` is the all-gathered normalized
+        activation of all ``Tg`` rows (reference: SP prefill, model/llama3/model.py:527-532,
+        813-815,1096-1111; nn/embedding.py:236-241)."""
+        tp = self.tp
+        use_sp = (self.sequence_parallel and tp.world > 1 and not small and b.embed_rows is None
+                  and not self.aux_layers)
+        if not use_sp:
+            self._sp = None
+            res = self.ws_residual[:T]
+            x = self.ws_x[:T]
+            ops.embedding(b.input_ids, self.embed, self.vocab_start, self.vocab_start + self.V_local,
+                          out=res, last_tok=b.last_tok)
+            tp.all_reduce_(res)
+            if b.embed_rows is not None:
+                res.index_copy_(0, b.embed_rows, b.embeds.to(res.dtype))
+            ops.rmsnorm(res, self.layers[0].input_norm, self.eps, out=x)
+            return res, x, T
+        W = tp.world
+        Tg = -(-T // W) * W
+        Tl = Tg // W
+        self._sp = (Tg, Tl)
+        self.sp_forwards += 1
+        full = self.ws_h[:Tg]
+        ops.embedding(b.input_ids, self.embed, self.vocab_start, self.vocab_start + self.V_local,
+                      out=full[:T], last_tok=b.last_tok)
+        if Tg > T:
+            full[T:].zero_()
+        res = self.ws_residual[:Tl]
+        tp.reduce_scatter(full, out=res)
+        x_l = self.ws_sp_x[:Tl]
+        ops.rmsnorm(res, self.layers[0].input_norm, self.eps, out=x_l)
+        x = self.ws_x[:Tg]
+        tp.all_gather(x_l, dim=0, out=x)
+        return res, x, Tg
+
+    def _reduce_norm(self, h: torch.Tensor, res: torch.Tensor, norm_w: torch.Tensor, x: torch.Tensor):
+        """Prefill row-parallel epilogue: ``res += sum_ranks(h)``; ``x = rmsnorm(res) * w``.
+        All-reduce, or under sequence parallelism reduce-scatter -> local add + RMSNorm ->
+        all-gather (same bytes on the wire, norms on 1/W of the rows)."""
+        if self._sp is None:
+            self.tp.all_reduce_(h)
+            ops.add_rmsnorm(h, res, norm_w, self.eps, out=x)
+            return
+        Tg, Tl = self._sp
+        h_l = self.ws_sp_h[:Tl]
+        self.tp.reduce_scatter(h[:Tg], out=h_l)
+        x_l = self.ws_sp_x[:Tl]
+        ops.add_rmsnorm(h_l, res, norm_w, self.eps, out=x_l)
+        self.tp.all_gather(x_l, dim=0, out=x[:Tg])
 
     def enable_aux_hidden(self, layers: list[int]):
         """Capture the residual stream after ``layers`` in every forward (draft models)."""
@@ -276,8 +335,7 @@ class LlamaForCausalLM(torch.nn.Module):
                 gu = L.gemm_out(x, ly.gate_up)
                 act = ops.silu_mul(gu, out=self.ws_act[:T])
             h = L.gemm_out(act, ly.down, out=self.ws_h[:T])
-            self.tp.all_reduce_(h)
-            ops.add_rmsnorm(h, res, nxt_norm, self.eps, out=x)
+            self._reduce_norm(h, res, nxt_norm, x)
 
     def _allreduce_norm(self, acc, res, norm_w, x, fused: bool):
         """Decode-size row-parallel epilogue: ``res += all_reduce(acc)``, ``x = rmsnorm(res)``."""

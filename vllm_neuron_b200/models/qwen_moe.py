@@ -42,7 +42,7 @@ class MoEMixin:
         self.e_start = self.tp.rank * self.e_local
         self.moe_ws = None
         if self.device.type == "cuda":
-            self.moe_ws = M.MoEWorkspace.create(self.max_tokens, self.topk, self.E, self.e_local, self.H,
+            self.moe_ws = M.MoEWorkspace.create(self.max_tokens + self.tp.world, self.topk, self.E, self.e_local, self.H,
                                                 self.I_moe, self.device, shared_inter=self.I_sh)
 
     def _moe_params(self, m, p):
@@ -60,8 +60,7 @@ class MoEMixin:
         M.moe_block(x, ly.router, ly.w_gu, ly.w_down, self.topk, self.route_mode, self.renorm,
                     act=self.expert_act, e_start=self.e_start, ws=self.moe_ws, out=h,
                     num_experts=self.E, shared_gu=ly.sh_gu, shared_down=ly.sh_down)
-        self.tp.all_reduce_(h)
-        ops.add_rmsnorm(h, res, nxt_norm, self.eps, out=x)
+        self._reduce_norm(h, res, nxt_norm, x)
 
 
 class Qwen3MoeForCausalLM(MoEMixin, LlamaForCausalLM):
