@@ -602,6 +602,17 @@ void moe_mxfp4_gemm(const at::Tensor& x, const at::Tensor& wt, at::Tensor& out,
   check_launch("moe_mxfp4_gemm");
 }
 
+// Bounded wait on flag[0] >= target for timeout_ms (failure-detection test of the peer waits).
+void flag_wait_probe(const at::Tensor& flag, int64_t target, double timeout_ms, at::Tensor& result) {
+  CHECK_CUDA(flag);
+  TORCH_CHECK(flag.scalar_type() == at::kInt && result.scalar_type() == at::kInt, "int32 tensors");
+  const c10::cuda::CUDAGuard guard(flag.device());
+  b200::flag_wait_probe_launch(reinterpret_cast<const unsigned int*>(flag.data_ptr<int>()), (unsigned)target,
+                               (unsigned long long)(timeout_ms * 1e6), status_word(), result.data_ptr<int>(),
+                               cur_stream());
+  check_launch("flag_wait_probe");
+}
+
 int64_t num_sms() { return b200::num_sms_cached(); }
 int64_t launch_count() { return g_launches.load(); }
 
@@ -618,6 +629,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sample", &sample);
   m.def("argmax", &argmax);
   m.def("read_status", &read_status);
+  m.def("flag_wait_probe", &flag_wait_probe);
   m.def("reset_status", &reset_status);
   m.def("num_sms", &num_sms);
   m.def("launch_count", &launch_count);

@@ -36,5 +36,7 @@ struct TPArNormParams {
 };
 
 void tp_allreduce_norm_launch(const TPArNormParams& p, cudaStream_t stream);
+void flag_wait_probe_launch(const unsigned int* flag, unsigned int target, unsigned long long timeout_ns,
+                            uint32_t* status, int* result, cudaStream_t stream);
 
 }  // namespace b200

@@ -39,14 +39,16 @@ __device__ __forceinline__ void st_release_sys_u32(unsigned int* p, unsigned int
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Returns false (and records `code`) if *f did not reach `target` in time.
+// Returns false (and records `code`) if *f did not reach `target` within `timeout_ns`, or at
+// once when an earlier wait already failed (status word set: fail fast, peers out of step).
 __device__ __forceinline__ bool wait_flag(const unsigned int* f, unsigned int target,
-                                          uint32_t* status, uint32_t code) {
+                                          uint32_t* status, uint32_t code,
+                                          uint64_t timeout_ns = B200_WAIT_TIMEOUT_NS) {
   if ((int)(ld_acquire_sys_u32(f) - target) >= 0) return true;
   if (status != nullptr && *reinterpret_cast<volatile uint32_t*>(status) != 0u) return false;
   const uint64_t t0 = globaltimer_ns();
   while ((int)(ld_acquire_sys_u32(f) - target) < 0) {
-    if (globaltimer_ns() - t0 > B200_WAIT_TIMEOUT_NS) {
+    if (globaltimer_ns() - t0 > timeout_ns) {
       set_status(status, code);
       return false;
     }
@@ -177,6 +179,22 @@ __global__ void __launch_bounds__(256) tp_allreduce_norm_kernel(const TPArNormPa
       p.state[0] = (unsigned long long)e + 1ull;
     }
   }
+}
+
+// One-thread probe of the fused collectives' bounded peer-flag wait (failure-detection test):
+// waits for *flag to reach `target` for at most `timeout_ns`; a flag that no peer sets makes
+// the wait expire, record kTimeoutPeerFlag in the status word and return -- the context stays
+// usable.  result[0] = 1 if the flag arrived, 0 if the wait gave up.
+__global__ void flag_wait_probe_kernel(const unsigned int* flag, unsigned int target,
+                                       unsigned long long timeout_ns, uint32_t* status, int* result) {
+  if (threadIdx.x == 0 && blockIdx.x == 0)
+    *result = wait_flag(flag, target, status, kTimeoutPeerFlag, timeout_ns) ? 1 : 0;
+}
+
+void flag_wait_probe_launch(const unsigned int* flag, unsigned int target, unsigned long long timeout_ns,
+                            uint32_t* status, int* result, cudaStream_t stream) {
+  if (timeout_ns > 5000000000ull) throw std::invalid_argument("flag_wait_probe: timeout above 5 s");
+  flag_wait_probe_kernel<<<1, 32, 0, stream>>>(flag, target, timeout_ns, status, result);
 }
 
 void tp_allreduce_norm_launch(const TPArNormParams& p, cudaStream_t stream) {

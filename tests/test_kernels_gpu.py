@@ -293,3 +293,34 @@ def test_apply_token_bitmask(cuda_device):
     apply_token_bitmask(ref, mask)
     apply_token_bitmask(logits, mask.to(cuda_device))
     assert torch.equal(torch.isinf(logits.cpu().float()), torch.isinf(ref))
+
+
+def test_bounded_peer_wait_expires_and_context_survives(cuda_device):
+    """A fused-collective flag wait whose flag nothing sets gives up after its budget, records
+    the peer-flag timeout code in the status word and returns; the context keeps working."""
+    import time
+
+    from vllm_neuron_b200.ops._ext import ext
+
+    e = ext()
+    e.reset_status()
+    flag = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    result = torch.full((1,), -1, dtype=torch.int32, device=cuda_device)
+    t0 = time.perf_counter()
+    e.flag_wait_probe(flag, 1, 100.0, result)  # 100 ms budget, nobody sets the flag
+    torch.cuda.synchronize()
+    dt = time.perf_counter() - t0
+    assert int(result.item()) == 0
+    assert e.read_status() == 5  # kTimeoutPeerFlag
+    assert dt < 5.0
+    e.reset_status()
+    flag.fill_(1)
+    e.flag_wait_probe(flag, 1, 100.0, result)
+    torch.cuda.synchronize()
+    assert int(result.item()) == 1 and e.read_status() == 0
+    # the context is intact: an ordinary kernel still runs and is correct
+    x = torch.randn(64, 256, device=cuda_device, dtype=torch.bfloat16)
+    w = torch.ones(256, device=cuda_device, dtype=torch.bfloat16)
+    y = ops.rmsnorm(x, w, 1e-5)
+    ref = (x.float() * torch.rsqrt(x.float().pow(2).mean(-1, keepdim=True) + 1e-5))
+    assert torch.allclose(y.float(), ref, atol=3e-2, rtol=3e-2)

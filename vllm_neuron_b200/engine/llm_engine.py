@@ -159,6 +159,15 @@ class LLMEngine:
         if args.speculative_config:
             self.proposer = self._make_proposer(dict(args.speculative_config))
             self.async_scheduling = False  # drafts depend on the previous step's tokens
+        self.monitor = None
+        self._last_peer_check = 0.0
+        if tp.world > 1 and tp.group is not None and envs.VLLM_B200_HEARTBEAT_TIMEOUT:
+            from ..parallel.health import PeerMonitor
+
+            store = torch.distributed.distributed_c10d._get_default_store()
+            self.monitor = PeerMonitor(store, torch.distributed.get_rank(), torch.distributed.get_world_size(),
+                                       interval_s=envs.VLLM_B200_HEARTBEAT_INTERVAL,
+                                       timeout_s=envs.VLLM_B200_HEARTBEAT_TIMEOUT)
 
     # ---------------------------------------------------------------- requests
     def add_request(self, prompt_token_ids: list[int], params: SamplingParams | None = None,
@@ -395,6 +404,14 @@ class LLMEngine:
     def step(self) -> list[Request]:
         """Schedule and launch the next step; with asynchronous scheduling the results of the
         previous step are processed while this one runs on the GPU."""
+        if self.monitor is not None:
+            # a peer that left (or went silent) is reported before this step launches
+            now = time.perf_counter()
+            if now - self._last_peer_check >= self.monitor.interval:
+                self._last_peer_check = now
+                self.monitor.check()
+            else:
+                self.monitor.check_fast()
         if self.proposer is not None:
             return self._spec_step()
         if self._has_structured and any(getattr(r, "matcher", None) is not None
@@ -438,4 +455,6 @@ class LLMEngine:
                              req.status.finished, m)
 
     def shutdown(self):
+        if self.monitor is not None:
+            self.monitor.stop(announce_exit=True)
         self.runner.release_graphs()

@@ -72,6 +72,9 @@ _flag("FP4_DECODE_MAX_TOKENS", _int, 64,
 _flag("PROFILE_DIR", _str, "b200_profile", "output directory of start_profile()/stop_profile()")
 _flag("SNAPSHOT_DIR", _str, None, "write the packed inputs of every engine step here (replay/debug)")
 _flag("SNAPSHOT_MAX_STEPS", _int, 64, "number of steps captured into SNAPSHOT_DIR")
+_flag("HEARTBEAT_TIMEOUT", _float, None,
+      "TP > 1: seconds without a peer heartbeat before a step raises PeerFailureError (off if unset)")
+_flag("HEARTBEAT_INTERVAL", _float, 0.5, "seconds between heartbeats / peer checks")
 _flag("WORKER_TERMINATION_TIMEOUT", _float, 30.0, "seconds shutdown waits for workers")
 
 
