@@ -184,11 +184,43 @@ def bench_moe(tp: int):
     return rows
 
 
+def bench_deltanet(tp: int):
+    """Gated DeltaNet layer of the Qwen3.6-A3B shape (16 key / 32 value heads x 128) per TP
+    shard: prefill of 8 x 1024 tokens (one 8192-token chunk) and a 64-sequence decode step.
+    Time covers the q/k normalisation pass, the recurrence and the gated RMSNorm."""
+    from vllm_neuron_b200.ops import deltanet as DN
+
+    Hk, Hv, d = 16 // tp, 32 // tp, 128
+    dev = "cuda"
+    rows = []
+    for name, q_lens, ctx in (("prefill_8x1024", [1024] * 8, [0] * 8), ("decode_b64", [1] * 64, [2048] * 64)):
+        B = len(q_lens)
+        qs = torch.tensor([0] + list(np.cumsum(q_lens)), dtype=torch.int32, device=dev)
+        sl = torch.tensor([a + b for a, b in zip(q_lens, ctx)], dtype=torch.int32, device=dev)
+        slots = torch.arange(B, dtype=torch.int32, device=dev)
+        T = sum(q_lens)
+        qkv = torch.randn(T, 2 * Hk * d + Hv * d, device=dev).to(torch.bfloat16)
+        zab = torch.randn(T, Hv * d + 2 * Hv, device=dev).to(torch.bfloat16)
+        z, b, a = zab[:, :Hv * d], zab[:, Hv * d:Hv * d + Hv], zab[:, Hv * d + Hv:]
+        A_log = torch.rand(Hv, device=dev).add(0.5).log()
+        dt_bias = torch.zeros(Hv, device=dev)
+        nw = torch.ones(d, device=dev, dtype=torch.bfloat16)
+        state = torch.zeros(B, Hv, d, d, device=dev)
+        out = torch.empty(T, Hv * d, device=dev, dtype=torch.bfloat16)
+        ms = timeit(lambda: DN.gated_delta_rule(qkv, z, a, b, A_log, dt_bias, nw, 1e-6, qs, sl, slots,
+                                                state, out, Hk, Hv))
+        r = {"op": "gated_delta_rule", "case": name, "tp": tp, "T": T, "ms": ms,
+             "us_per_token_step": ms * 1e3 / max(q_lens)}
+        print(json.dumps(r), flush=True)
+        rows.append(r)
+    return rows
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--tp", type=int, default=1)
     ap.add_argument("--json", type=str, default=None)
-    ap.add_argument("--only", type=str, default="gemm,decode,prefill,moe")
+    ap.add_argument("--only", type=str, default="gemm,decode,prefill,moe,deltanet")
     a = ap.parse_args()
     torch.manual_seed(0)
     rows = []
@@ -201,6 +233,8 @@ def main():
         rows += bench_prefill_attention(a.tp)
     if "moe" in only:
         rows += bench_moe(a.tp)
+    if "deltanet" in only:
+        rows += bench_deltanet(a.tp)
     if a.json:
         with open(a.json, "w") as f:
             json.dump(rows, f, indent=1)

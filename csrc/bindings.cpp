@@ -191,8 +191,9 @@ void rope_kv_write(at::Tensor& qkv, const at::Tensor& positions,
                    c10::optional<at::Tensor> v_cache, c10::optional<at::Tensor> q_norm_w,
                    c10::optional<at::Tensor> k_norm_w, double eps, int64_t num_q_heads,
                    int64_t num_kv_heads, int64_t head_dim, int64_t rot_dim, bool neox,
-                   bool clear_input) {
+                   bool clear_input, double q_pos_beta, double q_pos_period) {
   CHECK_CUDA(qkv);
+  TORCH_CHECK(q_pos_beta == 0.0 || q_pos_period > 0.0, "rope_kv_write: q_pos_period must be positive");
   const c10::cuda::CUDAGuard guard(qkv.device());
   b200::RopeKvParams p{};
   p.positions = positions.data_ptr<int>();
@@ -221,6 +222,8 @@ void rope_kv_write(at::Tensor& qkv, const at::Tensor& positions,
   p.rot_dim = (int)rot_dim;
   p.neox = neox;
   p.clear_input = clear_input;
+  p.q_pos_beta = (float)q_pos_beta;
+  p.q_pos_period = (float)(q_pos_period > 0.0 ? q_pos_period : 1.0);
   b200::rope_kv_write_launch(p, qkv.data_ptr(), qkv.scalar_type() == at::kFloat,
                              (int)qkv.size(0), cur_stream());
   check_launch("rope_kv_write");
@@ -532,7 +535,8 @@ void gated_delta_rule(const at::Tensor& qkv, const at::Tensor& z, const at::Tens
   TORCH_CHECK(z.stride(0) == a.stride(0) && z.stride(0) == b.stride(0), "z, a, b must share a row stride");
   const c10::cuda::CUDAGuard guard(qkv.device());
   b200::GatedDeltaParams p{};
-  p.qkv = reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr());
+  // q and k are l2-normalised in place: qkv is the conv output scratch of this layer
+  p.qkv = reinterpret_cast<__nv_bfloat16*>(qkv.data_ptr());
   p.ld_qkv = qkv.stride(0);
   p.z = reinterpret_cast<const __nv_bfloat16*>(z.data_ptr());
   p.a = reinterpret_cast<const __nv_bfloat16*>(a.data_ptr());
@@ -551,8 +555,11 @@ void gated_delta_rule(const at::Tensor& qkv, const at::Tensor& z, const at::Tens
   p.dk = (int)state.size(2);
   p.dv = (int)state.size(3);
   p.T = (int)out.size(0);
+  at::Tensor gb = at::empty({std::max<int64_t>(p.T, 1), Hv, 2}, qkv.options().dtype(at::kFloat));
+  p.gb = reinterpret_cast<float2*>(gb.data_ptr<float>());
   b200::gated_delta_rule_launch(p, linear_batch(q_start, seq_lens, slots), cur_stream());
-  check_launch("gated_delta_rule", seq_lens.size(0) > 0 ? 1 : 0);
+  // normalisation / gates pass, recurrence, gated RMSNorm
+  check_launch("gated_delta_rule", seq_lens.size(0) > 0 ? (p.T > 0 ? 3 : 1) : 0);
 }
 
 void sigmoid_gate_mul(at::Tensor& x, const at::Tensor& gate) {

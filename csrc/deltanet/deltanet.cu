@@ -13,11 +13,12 @@
 //
 //   causal_conv1d      one thread per channel, a sliding window of K - 1 inputs in registers,
 //                      loads of the step's tokens unrolled so they are in flight together.
-//   gated_delta_rule   per (sequence, value head, 16 value columns) one CTA of 4 warps; a warp
-//                      keeps 4 columns of S in registers (16 rows per lane) and reduces over
-//                      dk with shuffles, so tokens are processed in order (the recurrence)
-//                      without CTA barriers, next-token inputs prefetched; the gated RMSNorm
-//                      over dv runs afterwards (one warp per token and head).
+//   gated_delta_rule   a per-token pass normalises q, k in place and computes the gates; then
+//                      per (sequence, value head, 32 value columns) one CTA of 4 warps; a warp
+//                      keeps 8 columns of S in registers (16 rows x 2 columns per lane) and
+//                      reduces over dk with shuffles, so tokens are processed in order (the
+//                      recurrence) without CTA barriers, next-token inputs prefetched; the
+//                      gated RMSNorm over dv runs afterwards (one warp per token and head).
 #include <cuda_bf16.h>
 
 #include <stdexcept>
@@ -76,13 +77,41 @@ __global__ void __launch_bounds__(128) causal_conv1d_kernel(
   for (int j = 0; j < K - 1; ++j) st[j] = __float2bfloat16(win[j]);
 }
 
+// Per token: q and k of every key head l2-normalised in place (bf16, as the reference computes
+// the norm in the activation dtype), and the decay / write strength of every value head,
+// gb[t, h] = (g, beta) with g = exp(-exp(A_log) * softplus(a + dt_bias)), beta = sigmoid(b).
+// Hoisting these out of the recurrence removes work every value column used to repeat.
+__global__ void __launch_bounds__(256) gdn_prepare_kernel(const GatedDeltaParams p) {
+  pdl_trigger();
+  pdl_wait();
+  const long long t = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __nv_bfloat16* row = p.qkv + t * p.ld_qkv;
+  for (int h = warp; h < 2 * p.Hk; h += blockDim.x >> 5) {  // q heads then k heads
+    uint2* ptr = reinterpret_cast<uint2*>(row + (long long)h * 128 + lane * 4);
+    const uint2 u = *ptr;
+    const float2 f0 = unpack_bf16x2(u.x), f1 = unpack_bf16x2(u.y);
+    float ss = f0.x * f0.x + f0.y * f0.y + f1.x * f1.x + f1.y * f1.y;
+    ss = warp_sum(ss);
+    const float inv = rsqrtf(ss + 1e-6f);
+    *ptr = make_uint2(pack_bf16x2(f0.x * inv, f0.y * inv), pack_bf16x2(f1.x * inv, f1.y * inv));
+  }
+  for (int h = threadIdx.x; h < p.Hv; h += blockDim.x) {
+    const float a = __bfloat162float(p.a[t * p.ld_zab + h]);
+    const float bb = __bfloat162float(p.b[t * p.ld_zab + h]);
+    const float g = __expf(-__expf(p.A_log[h]) * softplus_d(a + p.dt_bias[h]));
+    p.gb[t * p.Hv + h] = make_float2(g, 1.f / (1.f + __expf(-bb)));
+  }
+}
+
 // dk = dv = 128.  The recurrence of value column v only reads column v of S, so columns are
-// independent: a warp owns 4 columns, lane = 8 * c + kg holds rows [16 kg, 16 kg + 16) of
-// column c (16 state floats).  Every k-reduction (the l2 norms of q and k, S^T k and S^T q)
-// is 3 butterfly shuffles inside the warp, so a token costs no CTA barrier; the next token's
-// inputs are loaded while the current one is processed.  Output: the un-normalised o (bf16),
-// normalised afterwards by gated_rmsnorm_kernel.  4 warps per CTA = 16 columns.
-constexpr int kGdnColsPerWarp = 4;
+// independent: lane = 8 * c + kg holds rows [16 kg, 16 kg + 16) of the two columns 2c, 2c + 1
+// of its warp's 8 (32 state floats), so one unpack of the token's q and k serves two columns.
+// Every k-reduction (S^T k and S^T q) is 3 butterfly shuffles inside the warp: a token costs
+// no CTA barrier; the next token's inputs are loaded while the current one is processed.
+// Output: the un-normalised o (bf16), normalised afterwards by gated_rmsnorm_kernel.
+// 4 warps per CTA = 32 columns.
+constexpr int kGdnColsPerWarp = 8;
 constexpr int kGdnWarps = 4;
 
 __global__ void __launch_bounds__(128) gated_delta_rule_kernel(const GatedDeltaParams p,
@@ -95,24 +124,28 @@ __global__ void __launch_bounds__(128) gated_delta_rule_kernel(const GatedDeltaP
   const int h = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kg = lane & 7;
-  const int v = (blockIdx.z * kGdnWarps + warp) * kGdnColsPerWarp + (lane >> 3);
+  const int v0 = (blockIdx.z * kGdnWarps + warp) * kGdnColsPerWarp + 2 * (lane >> 3);
   const int kh = h / (p.Hv / p.Hk);
   const int t0 = bt.q_start[b];
   const int n = bt.q_start[b + 1] - t0;
   const int ctx = bt.seq_lens[b] - n;
   float* S = p.state + (long long)bt.slots[b] * p.state_slot_stride + (long long)h * DK * DV;
-  float s[R];
+  float s0[R], s1[R];
 #pragma unroll
-  for (int r = 0; r < R; ++r) s[r] = ctx > 0 ? S[(long long)(kg * R + r) * DV + v] : 0.f;
-  const float A = -__expf(p.A_log[h]);
-  const float dtb = p.dt_bias[h];
+  for (int r = 0; r < R; ++r) {
+    float2 sv = make_float2(0.f, 0.f);
+    if (ctx > 0) sv = *reinterpret_cast<const float2*>(S + (long long)(kg * R + r) * DV + v0);
+    s0[r] = sv.x;
+    s1[r] = sv.y;
+  }
   const float qscale = rsqrtf((float)DK);
   const long long q_off = (long long)kh * DK + kg * R;
   const long long k_off = (long long)p.Hk * DK + q_off;
-  const long long v_off = 2LL * p.Hk * DK + (long long)h * DV + v;
+  const long long v_off = 2LL * p.Hk * DK + (long long)h * DV + v0;
 
   uint4 nq[2], nk[2];
-  float nv = 0.f, na = 0.f, nb = 0.f;
+  uint32_t nv = 0;
+  float2 ngb = make_float2(0.f, 0.f);
   auto load = [&](long long t) {
     const uint4* q4 = reinterpret_cast<const uint4*>(p.qkv + t * p.ld_qkv + q_off);
     const uint4* k4 = reinterpret_cast<const uint4*>(p.qkv + t * p.ld_qkv + k_off);
@@ -120,9 +153,8 @@ __global__ void __launch_bounds__(128) gated_delta_rule_kernel(const GatedDeltaP
     nq[1] = q4[1];
     nk[0] = k4[0];
     nk[1] = k4[1];
-    nv = __bfloat162float(p.qkv[t * p.ld_qkv + v_off]);
-    na = __bfloat162float(p.a[t * p.ld_zab + h]);
-    nb = __bfloat162float(p.b[t * p.ld_zab + h]);
+    nv = *reinterpret_cast<const uint32_t*>(p.qkv + t * p.ld_qkv + v_off);
+    ngb = p.gb[t * p.Hv + h];
   };
   if (n > 0) load(t0);
   for (int i = 0; i < n; ++i) {
@@ -141,44 +173,42 @@ __global__ void __launch_bounds__(128) gated_delta_rule_kernel(const GatedDeltaP
         k[8 * j + 2 * e + 1] = fk.y;
       }
     }
-    const float vt = nv, a = na, bb = nb;
+    const float2 vt = unpack_bf16x2(nv);
+    const float g = ngb.x, beta = ngb.y;
     if (i + 1 < n) load(t + 1);
-    float sq = 0.f, sk = 0.f;
+    // kv = (g S)^T k for both columns
+    float kv0 = 0.f, kv1 = 0.f;
 #pragma unroll
     for (int r = 0; r < R; ++r) {
-      sq += q[r] * q[r];
-      sk += k[r] * k[r];
+      kv0 += s0[r] * k[r];
+      kv1 += s1[r] * k[r];
     }
 #pragma unroll
     for (int o = 1; o < 8; o <<= 1) {
-      sq += __shfl_xor_sync(FULL, sq, o);
-      sk += __shfl_xor_sync(FULL, sk, o);
+      kv0 += __shfl_xor_sync(FULL, kv0, o);
+      kv1 += __shfl_xor_sync(FULL, kv1, o);
     }
-    const float iq = rsqrtf(sq + 1e-6f) * qscale, ik = rsqrtf(sk + 1e-6f);
-    const float g = __expf(A * softplus_d(a + dtb));
-    const float beta = 1.f / (1.f + __expf(-bb));
-    float kv = 0.f;
+    const float d0 = (vt.x - g * kv0) * beta, d1 = (vt.y - g * kv1) * beta;
+    float o0 = 0.f, o1 = 0.f;
 #pragma unroll
     for (int r = 0; r < R; ++r) {
-      k[r] *= ik;
-      s[r] *= g;
-      kv += s[r] * k[r];
+      s0[r] = fmaf(g, s0[r], k[r] * d0);
+      s1[r] = fmaf(g, s1[r], k[r] * d1);
+      o0 += s0[r] * q[r];
+      o1 += s1[r] * q[r];
     }
 #pragma unroll
-    for (int o = 1; o < 8; o <<= 1) kv += __shfl_xor_sync(FULL, kv, o);
-    const float delta = (vt - kv) * beta;
-    float ov = 0.f;
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      s[r] += k[r] * delta;
-      ov += s[r] * q[r];
+    for (int o = 1; o < 8; o <<= 1) {
+      o0 += __shfl_xor_sync(FULL, o0, o);
+      o1 += __shfl_xor_sync(FULL, o1, o);
     }
-#pragma unroll
-    for (int o = 1; o < 8; o <<= 1) ov += __shfl_xor_sync(FULL, ov, o);
-    if (kg == 0) p.out[t * p.ld_out + (long long)h * DV + v] = __float2bfloat16(ov * iq);
+    if (kg == 0)
+      *reinterpret_cast<uint32_t*>(p.out + t * p.ld_out + (long long)h * DV + v0) =
+          pack_bf16x2(o0 * qscale, o1 * qscale);
   }
 #pragma unroll
-  for (int r = 0; r < R; ++r) S[(long long)(kg * R + r) * DV + v] = s[r];
+  for (int r = 0; r < R; ++r)
+    *reinterpret_cast<float2*>(S + (long long)(kg * R + r) * DV + v0) = make_float2(s0[r], s1[r]);
 }
 
 // out[t, h, :] = w * rmsnorm(out[t, h, :]) * silu(z[t, h, :]) over dv = 128 (one warp per row;
@@ -252,6 +282,7 @@ void gated_delta_rule_launch(const GatedDeltaParams& p, const LinearAttnBatch& b
   if (p.ld_qkv % 8 != 0 || p.ld_zab % 4 != 0 || p.ld_out % 4 != 0)
     throw std::invalid_argument("gated_delta_rule: row strides must allow vector loads");
   if (b.B == 0) return;
+  if (p.T > 0) launch_pdl(gdn_prepare_kernel, dim3(p.T), dim3(256), 0, s, p);
   constexpr int cols_per_cta = kGdnWarps * kGdnColsPerWarp;
   launch_pdl(gated_delta_rule_kernel, dim3(b.B, p.Hv, 128 / cols_per_cta), dim3(32 * kGdnWarps), 0,
              s, p, b);

@@ -27,6 +27,9 @@ struct RopeKvParams {
   int Hq, Hkv, head_dim, rot_dim, block_size;
   bool neox;
   bool clear_input;
+  // q *= 1 + q_pos_beta * log(1 + floor(pos / q_pos_period)) after rotation (0: off)
+  float q_pos_beta;
+  float q_pos_period;
 };
 void rope_kv_write_launch(const RopeKvParams& p, void* qkv, bool qkv_is_f32, int T,
                           cudaStream_t stream);

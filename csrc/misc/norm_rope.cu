@@ -268,8 +268,13 @@ __global__ void __launch_bounds__(256) rope_kv_write_kernel(const RopeKvParams p
     }
     if (is_q) {
       __nv_bfloat16* dst = p.q_out + (long long)t * p.q_out_stride + (long long)h * D;
+      // position-dependent query temperature (long-context scaling of the Llama-4 / Ministral-3
+      // families)
+      const float qs = p.q_pos_beta != 0.f
+                           ? 1.f + p.q_pos_beta * logf(1.f + floorf((float)pos / p.q_pos_period))
+                           : 1.f;
 #pragma unroll
-      for (int e = 0; e < PER; ++e) dst[lane + 32 * e] = __float2bfloat16(v[e]);
+      for (int e = 0; e < PER; ++e) dst[lane + 32 * e] = __float2bfloat16(v[e] * qs);
     } else if (slot >= 0) {
       const int kvh = is_k ? h - p.Hq : h - p.Hq - p.Hkv;
       const long long blk = slot / p.block_size, off = slot % p.block_size;

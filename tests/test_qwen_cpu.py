@@ -90,3 +90,21 @@ def test_qwen3_embedding_pooling():
         ref = torch.stack([hf(torch.tensor([p])).last_hidden_state[0, -1] for p in prompts])
     ref = torch.nn.functional.normalize(ref, dim=-1)
     assert torch.allclose(got, ref, atol=2e-3)  # the QK-norm output is rounded to bf16 as on the GPU
+
+
+def test_ministral3_yarn_and_query_temperature():
+    """Ministral-3 text model: YaRN (mscale / mscale_all_dim) and the position-dependent query
+    scale 1 + beta * log(1 + floor(pos / original_max)); a small original_max makes the scale
+    change inside the prompts."""
+    from transformers import Ministral3Config, Ministral3ForCausalLM
+
+    torch.manual_seed(4)
+    cfg = Ministral3Config(hidden_size=64, num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
+                           head_dim=16, intermediate_size=128, vocab_size=512, max_position_embeddings=256,
+                           initializer_range=0.05, tie_word_embeddings=False,
+                           rope_parameters={"rope_type": "yarn", "rope_theta": 1000000.0, "factor": 4.0,
+                                            "original_max_position_embeddings": 8, "beta_fast": 32.0,
+                                            "beta_slow": 1.0, "mscale": 1.0, "mscale_all_dim": 1.0,
+                                            "llama_4_scaling_beta": 0.5})
+    hf = Ministral3ForCausalLM(cfg).float().eval()
+    _check(_save(hf), hf, 512)

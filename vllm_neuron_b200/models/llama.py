@@ -108,6 +108,11 @@ class LlamaForCausalLM(torch.nn.Module):
         self.lm_head = self.embed if cfg.tie_word_embeddings else p(self.V_local, self.H)
         self.cos_sin = ops.cos_sin_table(cfg.max_position_embeddings, cfg.rot_dim, cfg.rope_theta,
                                          cfg.rope_scaling, device=self.device)
+        # long-context query temperature (Ministral-3: rope_parameters.llama_4_scaling_beta)
+        rp = cfg.rope_scaling or {}
+        beta = rp.get("llama_4_scaling_beta")
+        self.q_pos_scale = ((float(beta), float(rp.get("original_max_position_embeddings") or 8192))
+                            if beta else None)
         self.kv_caches: list[tuple[torch.Tensor, torch.Tensor]] = []
         self._alloc_workspace(max_tokens, max_decode_tokens, max_seqs)
         self.tp_fused = None  # TPFusedComm: fused all-reduce + residual + RMSNorm (decode)
@@ -222,14 +227,14 @@ class LlamaForCausalLM(torch.nn.Module):
                     acc.add_(ly.qkv_bias.float())
                 ops.rope_kv_write(acc, b.positions, self.cos_sin, self.Hq, self.Hkv, self.D, q,
                                   k_cache, v_cache, b.slot_mapping, ly.q_norm, ly.k_norm, self.eps,
-                                  rot_dim=self.cfg.rot_dim, clear_input=True)
+                                  rot_dim=self.cfg.rot_dim, clear_input=True, q_pos_scale=self.q_pos_scale)
             else:
                 qkv = L.gemm_out(x[:T], ly.qkv, out=self.ws_qkv[:T])
                 if ly.qkv_bias is not None:
                     qkv.add_(ly.qkv_bias)
                 ops.rope_kv_write(qkv, b.positions, self.cos_sin, self.Hq, self.Hkv, self.D, q,
                                   k_cache, v_cache, b.slot_mapping, ly.q_norm, ly.k_norm, self.eps,
-                                  rot_dim=self.cfg.rot_dim)
+                                  rot_dim=self.cfg.rot_dim, q_pos_scale=self.q_pos_scale)
             attn = self.ws_attn[:T]
             self._attention(q, attn, k_cache, v_cache, b, window=ly.window, sinks=ly.sinks)
             nxt_norm = ly.post_norm

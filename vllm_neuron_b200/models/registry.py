@@ -6,6 +6,8 @@ import importlib
 _MODELS = {
     "LlamaForCausalLM": ("vllm_neuron_b200.models.llama", "LlamaForCausalLM"),
     "MistralForCausalLM": ("vllm_neuron_b200.models.llama", "LlamaForCausalLM"),
+    "MinistralForCausalLM": ("vllm_neuron_b200.models.llama", "LlamaForCausalLM"),
+    "Ministral3ForCausalLM": ("vllm_neuron_b200.models.llama", "LlamaForCausalLM"),
     "Qwen3ForCausalLM": ("vllm_neuron_b200.models.llama", "LlamaForCausalLM"),
     "Qwen2ForCausalLM": ("vllm_neuron_b200.models.llama", "LlamaForCausalLM"),
     # embedding backbones (pooling through LLM.embed)

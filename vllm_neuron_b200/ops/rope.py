@@ -63,12 +63,17 @@ def cos_sin_table(max_pos: int, rot_dim: int, theta: float, scaling: dict | None
                               scaling.get("high_freq_factor", 4.0),
                               scaling.get("original_max_position_embeddings", 8192))
     elif kind == "yarn":
-        inv, mscale = inv_freq_yarn(rot_dim, theta, scaling["factor"],
-                                    scaling.get("original_max_position_embeddings", 4096),
-                                    scaling.get("beta_fast", 32.0), scaling.get("beta_slow", 1.0),
+        orig = scaling.get("original_max_position_embeddings", 4096)
+        factor = scaling.get("factor") or max_pos / orig
+        inv, mscale = inv_freq_yarn(rot_dim, theta, factor, orig,
+                                    scaling.get("beta_fast") or 32.0, scaling.get("beta_slow") or 1.0,
                                     scaling.get("truncate", True))
         if scaling.get("attention_factor") is not None:
             mscale = scaling["attention_factor"]
+        elif scaling.get("mscale") and scaling.get("mscale_all_dim"):
+            def _m(sc, m):
+                return 1.0 if sc <= 1 else 0.1 * m * math.log(sc) + 1.0
+            mscale = _m(factor, scaling["mscale"]) / _m(factor, scaling["mscale_all_dim"])
     else:
         inv = inv_freq_default(rot_dim, theta)
     pos = torch.arange(max_pos, dtype=torch.float64)
@@ -83,19 +88,23 @@ def rope_kv_write(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Ten
                   slot_mapping: torch.Tensor | None = None, q_norm_w: torch.Tensor | None = None,
                   k_norm_w: torch.Tensor | None = None, eps: float = 1e-6,
                   rot_dim: int | None = None, neox: bool = True,
-                  clear_input: bool = False) -> torch.Tensor:
+                  clear_input: bool = False, q_pos_scale: tuple[float, float] | None = None) -> torch.Tensor:
     """Rotate q/k of ``qkv [T, (Hq + 2 Hkv) * D]``; write rotated q to ``q_out [T, Hq * D]`` and
-    k/v into the paged cache at ``slot_mapping`` (int32, negative = skip)."""
+    k/v into the paged cache at ``slot_mapping`` (int32, negative = skip).  ``q_pos_scale =
+    (beta, period)`` multiplies the rotated q by ``1 + beta * log(1 + floor(pos / period))``
+    (the long-context query temperature of Ministral-3 / Llama-4 configs)."""
     rot_dim = rot_dim or head_dim
+    beta, period = q_pos_scale if q_pos_scale else (0.0, 1.0)
     if not qkv.is_cuda:
         rope_kv_write_ref(qkv, positions, cos_sin, num_q_heads, num_kv_heads, head_dim, q_out,
-                          k_cache, v_cache, slot_mapping, q_norm_w, k_norm_w, eps, rot_dim, neox)
+                          k_cache, v_cache, slot_mapping, q_norm_w, k_norm_w, eps, rot_dim, neox,
+                          q_pos_scale)
         if clear_input:
             qkv.zero_()
         return q_out
     ext().rope_kv_write(qkv, positions, slot_mapping, cos_sin, q_out, k_cache, v_cache,
                         q_norm_w, k_norm_w, eps, num_q_heads, num_kv_heads, head_dim, rot_dim,
-                        neox, clear_input and qkv.dtype == torch.float32)
+                        neox, clear_input and qkv.dtype == torch.float32, float(beta), float(period))
     return q_out
 
 
@@ -114,7 +123,7 @@ def apply_rope_ref(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, neox: 
 
 
 def rope_kv_write_ref(qkv, positions, cos_sin, Hq, Hkv, D, q_out, k_cache, v_cache,
-                      slot_mapping, q_norm_w, k_norm_w, eps, rot_dim, neox):
+                      slot_mapping, q_norm_w, k_norm_w, eps, rot_dim, neox, q_pos_scale=None):
     from .norm import rmsnorm_ref
 
     T = qkv.shape[0]
@@ -129,6 +138,10 @@ def rope_kv_write_ref(qkv, positions, cos_sin, Hq, Hkv, D, q_out, k_cache, v_cac
     cos, sin = cs[:, :half], cs[:, half:rot_dim]
     q = torch.cat([apply_rope_ref(q[..., :rot_dim], cos, sin, neox), q[..., rot_dim:]], -1)
     k = torch.cat([apply_rope_ref(k[..., :rot_dim], cos, sin, neox), k[..., rot_dim:]], -1)
+    if q_pos_scale and q_pos_scale[0]:
+        beta, period = q_pos_scale
+        sc = 1 + beta * torch.log1p(torch.floor(positions.double() / period))
+        q = q * sc.float()[:, None, None]
     q_out.view(T, Hq, D).copy_(q.to(q_out.dtype))
     if k_cache is not None and slot_mapping is not None:
         bs = k_cache.shape[2]
