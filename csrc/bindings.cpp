@@ -395,7 +395,7 @@ void gemm_grouped(const at::Tensor& x_perm, const at::Tensor& w, at::Tensor& out
 
 void moe_route(const at::Tensor& logits, c10::optional<at::Tensor> bias, int64_t num_experts,
                int64_t k, int64_t mode, bool renorm, at::Tensor& ids, at::Tensor& weights,
-               c10::optional<at::Tensor> shared_gate) {
+               c10::optional<at::Tensor> shared_gate, double scale) {
   CHECK_CUDA(logits);
   CHECK_BF16(logits);
   TORCH_CHECK(logits.stride(1) == 1, "moe_route: logits rows must be contiguous");
@@ -410,7 +410,7 @@ void moe_route(const at::Tensor& logits, c10::optional<at::Tensor> bias, int64_t
                          b, (int)logits.size(0), (int)num_experts, (int)k, (int)mode, renorm,
                          ids.data_ptr<int>(), weights.data_ptr<float>(),
                          shared_gate.has_value() ? shared_gate->data_ptr<float>() : nullptr,
-                         cur_stream());
+                         (float)scale, cur_stream());
   check_launch("moe_route", logits.size(0) > 0 ? 1 : 0);
 }
 

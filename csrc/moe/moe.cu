@@ -32,7 +32,7 @@ constexpr int kMaxExpertsPerLane = 16;  // E <= 512
 __global__ void moe_route_kernel(const __nv_bfloat16* __restrict__ logits, long long ld,
                                  const float* __restrict__ bias, int T, int E, int k, int mode,
                                  int renorm, int* __restrict__ ids, float* __restrict__ weights,
-                                 float* __restrict__ shared_gate) {
+                                 float* __restrict__ shared_gate, float scale) {
   pdl_trigger();
   pdl_wait();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -42,16 +42,25 @@ __global__ void moe_route_kernel(const __nv_bfloat16* __restrict__ logits, long 
   // column E (when present) is the shared expert's gate logit
   if (shared_gate != nullptr && lane == 0)
     shared_gate[warp] = 1.f / (1.f + __expf(-__bfloat162float(row[E])));
-  float v[kMaxExpertsPerLane];
+  const bool bias_after = mode == ROUTE_SIGMOID_BIAS_TOPK;  // bias only ranks the experts
+  float v[kMaxExpertsPerLane], raw[kMaxExpertsPerLane];
 #pragma unroll
   for (int i = 0; i < kMaxExpertsPerLane; ++i) {
     const int e = i * 32 + lane;
     float x = -INFINITY;
     if (e < E) {
       x = __bfloat162float(row[e]);
-      if (bias != nullptr) x += bias[e];
+      if (bias != nullptr && !bias_after) x += bias[e];
     }
     v[i] = x;
+  }
+  if (bias_after) {
+#pragma unroll
+    for (int i = 0; i < kMaxExpertsPerLane; ++i) {
+      const int e = i * 32 + lane;
+      raw[i] = e < E ? 1.f / (1.f + __expf(-v[i])) : 0.f;
+      v[i] = e < E ? raw[i] + (bias != nullptr ? bias[e] : 0.f) : -INFINITY;
+    }
   }
   // score transform before selection
   if (mode == ROUTE_SOFTMAX_TOPK) {
@@ -81,7 +90,7 @@ __global__ void moe_route_kernel(const __nv_bfloat16* __restrict__ logits, long 
   int sel_e = 0;
   float tot = 0.f, mx0 = 0.f;
   for (int r = 0; r < k; ++r) {
-    float bv = -INFINITY;
+    float bv = -INFINITY, braw = 0.f;
     int be = 0x7fffffff;
 #pragma unroll
     for (int i = 0; i < kMaxExpertsPerLane; ++i) {
@@ -89,15 +98,18 @@ __global__ void moe_route_kernel(const __nv_bfloat16* __restrict__ logits, long 
       if (e < E && (v[i] > bv || (v[i] == bv && e < be))) {
         bv = v[i];
         be = e;
+        if (bias_after) braw = raw[i];
       }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
       const int oe = __shfl_xor_sync(0xffffffffu, be, o);
+      const float oraw = __shfl_xor_sync(0xffffffffu, braw, o);
       if (ov > bv || (ov == bv && oe < be)) {
         bv = ov;
         be = oe;
+        braw = oraw;
       }
     }
     // remove the winner
@@ -105,7 +117,7 @@ __global__ void moe_route_kernel(const __nv_bfloat16* __restrict__ logits, long 
     for (int i = 0; i < kMaxExpertsPerLane; ++i)
       if (i * 32 + lane == be) v[i] = -INFINITY;
     if (lane == r) {
-      sel_v = bv;
+      sel_v = bias_after ? braw : bv;
       sel_e = be;
     }
     if (r == 0) mx0 = bv;
@@ -125,7 +137,7 @@ __global__ void moe_route_kernel(const __nv_bfloat16* __restrict__ logits, long 
   }
   if (lane < k) {
     ids[(long long)warp * k + lane] = sel_e;
-    weights[(long long)warp * k + lane] = w;
+    weights[(long long)warp * k + lane] = w * scale;
   }
 }
 
@@ -334,14 +346,14 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y,
 
 void moe_route_launch(const __nv_bfloat16* logits, long long ld, const float* bias, int T, int E,
                       int k, int mode, bool renorm, int* ids, float* weights, float* shared_gate,
-                      cudaStream_t s) {
+                      float scale, cudaStream_t s) {
   if (E > 32 * kMaxExpertsPerLane) throw std::invalid_argument("moe_route: at most 512 experts");
   if (k < 1 || k > 32 || k > E) throw std::invalid_argument("moe_route: 1 <= k <= min(32, E)");
   if (T == 0) return;
   const int warps_per_block = 4;
   launch_pdl(moe_route_kernel, dim3((T + warps_per_block - 1) / warps_per_block),
              dim3(32 * warps_per_block), 0, s, logits, ld, bias, T, E, k, mode, renorm ? 1 : 0, ids,
-             weights, shared_gate);
+             weights, shared_gate, scale);
 }
 
 void moe_align_launch(const int* ids, int n_assign, int e_start, int e_local, int* offsets,

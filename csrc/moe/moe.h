@@ -10,6 +10,8 @@ enum RouteMode : int {
   ROUTE_TOPK_SOFTMAX = 0,  // top-k of the logits, softmax over the k selected (GPT-OSS)
   ROUTE_SOFTMAX_TOPK = 1,  // softmax over all experts, top-k, optional renormalisation (Qwen)
   ROUTE_SIGMOID_TOPK = 2,  // sigmoid scores, top-k, optional renormalisation
+  ROUTE_SIGMOID_BIAS_TOPK = 3,  // top-k of sigmoid + correction bias; weights from the
+                                // unbiased sigmoid, optional renormalisation (GLM-4.5 MoE)
 };
 
 enum MoeAct : int {
@@ -20,9 +22,10 @@ enum MoeAct : int {
 
 // logits [T, E (+1)]: when shared_gate is given, column E is the shared expert's gate logit
 // and shared_gate[t] = sigmoid(logits[t, E]).
+// weights are multiplied by `scale` (routed scaling factor) after any renormalisation
 void moe_route_launch(const __nv_bfloat16* logits, long long ld, const float* bias, int T, int E,
                       int k, int mode, bool renorm, int* ids, float* weights, float* shared_gate,
-                      cudaStream_t s);
+                      float scale, cudaStream_t s);
 
 // Groups the T*k assignments by local expert [e_start, e_start + e_local).
 void moe_align_launch(const int* ids, int n_assign, int e_start, int e_local, int* offsets,

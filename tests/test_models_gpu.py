@@ -89,3 +89,39 @@ def test_qwen3_moe_gpu_matches_cpu(cuda_device):
     d = tempfile.mkdtemp(prefix="qwen3moe_gpu_")
     hf.save_pretrained(d, safe_serialization=True)
     _agree(d)
+
+
+def test_glm4_moe_gpu_matches_cpu(cuda_device):
+    from transformers import Glm4MoeConfig, Glm4MoeForCausalLM
+
+    torch.manual_seed(0)
+    cfg = Glm4MoeConfig(hidden_size=256, num_hidden_layers=3, num_attention_heads=4, num_key_value_heads=2,
+                        head_dim=64, intermediate_size=512, moe_intermediate_size=128, n_routed_experts=16,
+                        num_experts_per_tok=4, n_shared_experts=1, first_k_dense_replace=1,
+                        routed_scaling_factor=2.5, norm_topk_prob=True, attention_bias=True,
+                        use_qk_norm=True, partial_rotary_factor=0.5, vocab_size=1024,
+                        max_position_embeddings=1024, initializer_range=0.05)
+    hf = Glm4MoeForCausalLM(cfg).to(torch.bfloat16).eval()
+    with torch.no_grad():
+        for ly in hf.model.layers[1:]:
+            ly.mlp.gate.e_score_correction_bias.normal_(0.0, 0.1)
+    d = tempfile.mkdtemp(prefix="glm4moe_gpu_")
+    hf.save_pretrained(d, safe_serialization=True)
+    _agree(d)
+
+
+def test_ministral3_gpu_matches_cpu(cuda_device):
+    from transformers import Ministral3Config, Ministral3ForCausalLM
+
+    torch.manual_seed(0)
+    cfg = Ministral3Config(hidden_size=256, num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
+                           head_dim=64, intermediate_size=512, vocab_size=1024, max_position_embeddings=1024,
+                           initializer_range=0.05, tie_word_embeddings=False,
+                           rope_parameters={"rope_type": "yarn", "rope_theta": 1000000.0, "factor": 4.0,
+                                            "original_max_position_embeddings": 16, "beta_fast": 32.0,
+                                            "beta_slow": 1.0, "mscale": 1.0, "mscale_all_dim": 1.0,
+                                            "llama_4_scaling_beta": 0.1})
+    hf = Ministral3ForCausalLM(cfg).to(torch.bfloat16).eval()
+    d = tempfile.mkdtemp(prefix="ministral3_gpu_")
+    hf.save_pretrained(d, safe_serialization=True)
+    _agree(d)

@@ -25,20 +25,22 @@ def _status(cuda_device):
 
 
 @pytest.mark.parametrize("mode,renorm", [(M.ROUTE_TOPK_SOFTMAX, True), (M.ROUTE_SOFTMAX_TOPK, True),
-                                         (M.ROUTE_SOFTMAX_TOPK, False), (M.ROUTE_SIGMOID_TOPK, True)])
+                                         (M.ROUTE_SOFTMAX_TOPK, False), (M.ROUTE_SIGMOID_TOPK, True),
+                                         (M.ROUTE_SIGMOID_BIAS_TOPK, True), (M.ROUTE_SIGMOID_BIAS_TOPK, False)])
 @pytest.mark.parametrize("E,k", [(32, 4), (256, 8), (128, 1)])
 def test_route(cuda_device, mode, renorm, E, k):
     T = 300
     logits = (torch.randn(T, E, device=cuda_device) * 2).to(torch.bfloat16)
     bias = torch.randn(E, device=cuda_device) * 0.1
-    ids, w = M.route(logits, k, mode, renorm, bias)
-    rid, rw = M.route_ref(logits, k, mode, renorm, bias)
+    scale = 2.5 if mode == M.ROUTE_SIGMOID_BIAS_TOPK else 1.0
+    ids, w = M.route(logits, k, mode, renorm, bias, scale=scale)
+    rid, rw = M.route_ref(logits, k, mode, renorm, bias, scale)
     # compare as sets per token (the order of equal scores may differ)
     s_ids, o = torch.sort(ids.long(), -1)
     s_rid, ro = torch.sort(rid.long(), -1)
     assert (s_ids == s_rid).float().mean() > 0.99
     same = (s_ids == s_rid).all(-1)
-    assert torch.allclose(torch.gather(w, 1, o)[same], torch.gather(rw, 1, ro)[same], atol=2e-3)
+    assert torch.allclose(torch.gather(w, 1, o)[same], torch.gather(rw, 1, ro)[same], atol=2e-3 * scale)
 
 
 @pytest.mark.parametrize("T", [1, 7, 64, 300])
@@ -111,4 +113,24 @@ def test_moe_block_mxfp4_decode(cuda_device, T):
                       fp4_gu=fp4_gu, fp4_down=fp4_dn)
     ids, w = M.route_ref(ws.logits[:T, :E], k, M.ROUTE_TOPK_SOFTMAX)
     ref = M.experts_ref(x, ids, w, w_gu, w_dn, act=M.ACT_GPTOSS)
+    assert _rel_err(out, ref) < 2e-2
+
+
+@pytest.mark.parametrize("T", [3, 200])
+def test_moe_block_glm_routing_ungated_shared(cuda_device, T):
+    """GLM-4.5 MoE block: biased-sigmoid routing, routed scaling factor, ungated shared expert."""
+    E, k, H, I = 64, 8, 512, 256
+    g = torch.Generator(device=cuda_device).manual_seed(5)
+    x = torch.randn(T, H, device=cuda_device, generator=g).to(torch.bfloat16)
+    rw = (torch.randn(E, H, device=cuda_device, generator=g) * 0.05).to(torch.bfloat16)
+    rb = torch.randn(E, device=cuda_device, generator=g) * 0.1
+    w_gu = (torch.randn(E, 2 * I, H, device=cuda_device, generator=g) * H ** -0.5).to(torch.bfloat16)
+    w_dn = (torch.randn(E, H, I, device=cuda_device, generator=g) * I ** -0.5).to(torch.bfloat16)
+    s_gu = (torch.randn(2 * I, H, device=cuda_device, generator=g) * H ** -0.5).to(torch.bfloat16)
+    s_dn = (torch.randn(H, I, device=cuda_device, generator=g) * I ** -0.5).to(torch.bfloat16)
+    ws = M.MoEWorkspace.create(256, k, E, E, H, I, cuda_device, shared_inter=I)
+    out = M.moe_block(x, rw, w_gu, w_dn, k, M.ROUTE_SIGMOID_BIAS_TOPK, True, rb, ws=ws, num_experts=E,
+                      shared_gu=s_gu, shared_down=s_dn, routed_scale=2.5, shared_gated=False)
+    ids, w = M.route_ref(ws.logits[:T, :E], k, M.ROUTE_SIGMOID_BIAS_TOPK, True, rb, 2.5)
+    ref = M.experts_ref(x, ids, w, w_gu, w_dn) + M.shared_expert_ref(x, s_gu, s_dn)
     assert _rel_err(out, ref) < 2e-2

@@ -108,3 +108,26 @@ def test_ministral3_yarn_and_query_temperature():
                                             "llama_4_scaling_beta": 0.5})
     hf = Ministral3ForCausalLM(cfg).float().eval()
     _check(_save(hf), hf, 512)
+
+
+def test_glm4_moe():
+    """GLM-4.5-style MoE: dense first layer, biased-sigmoid routing with routed scaling,
+    ungated shared expert, q/k/v bias, partial rotary, QK-norm."""
+    from transformers import Glm4MoeConfig, Glm4MoeForCausalLM
+
+    torch.manual_seed(6)
+    cfg = Glm4MoeConfig(hidden_size=64, num_hidden_layers=3, num_attention_heads=4, num_key_value_heads=2,
+                        head_dim=16, intermediate_size=128, moe_intermediate_size=32, n_routed_experts=8,
+                        num_experts_per_tok=2, n_shared_experts=1, first_k_dense_replace=1,
+                        routed_scaling_factor=2.5, norm_topk_prob=True, n_group=1, topk_group=1,
+                        attention_bias=True, use_qk_norm=True, partial_rotary_factor=0.5,
+                        vocab_size=512, max_position_embeddings=256, initializer_range=0.05,
+                        tie_word_embeddings=False)
+    hf = Glm4MoeForCausalLM(cfg).float().eval()
+    with torch.no_grad():  # non-zero correction bias and attention biases
+        for ly in hf.model.layers[1:]:
+            ly.mlp.gate.e_score_correction_bias.normal_(0.0, 0.1)
+        for ly in hf.model.layers:
+            for m in (ly.self_attn.q_proj, ly.self_attn.k_proj, ly.self_attn.v_proj):
+                m.bias.normal_(0.0, 0.05)
+    _check(_save(hf), hf, 512)

@@ -95,11 +95,13 @@ class ModelArchConfig:
             partial_rotary_factor=cfg.get("partial_rotary_factor", rp.get("partial_rotary_factor", 1.0)),
             max_position_embeddings=cfg.get("max_position_embeddings", 8192),
             tie_word_embeddings=cfg.get("tie_word_embeddings", False),
-            qk_norm=cfg.get("model_type", "") in ("qwen3", "qwen3_moe", "qwen3_next", "qwen3_vl",
-                                                  "qwen3_5_moe", "qwen3_5_moe_text", "qwen3_5", "qwen3_5_text"),
+            qk_norm=(cfg.get("model_type", "") in ("qwen3", "qwen3_moe", "qwen3_next", "qwen3_vl",
+                                                   "qwen3_5_moe", "qwen3_5_moe_text", "qwen3_5", "qwen3_5_text")
+                     or bool(cfg.get("use_qk_norm", False))),
             attention_bias=cfg.get("attention_bias", cfg.get("qkv_bias",
                                                               cfg.get("model_type") in ("qwen2", "qwen2_moe"))),
-            num_experts=cfg.get("num_local_experts", cfg.get("num_experts", 0)) or 0,
+            num_experts=(cfg.get("num_local_experts") or cfg.get("num_experts")
+                         or cfg.get("n_routed_experts") or 0),
             num_experts_per_tok=cfg.get("num_experts_per_tok", cfg.get("experts_per_token", 0)) or 0,
             moe_intermediate_size=cfg.get("moe_intermediate_size", 0) or 0,
             shared_expert_intermediate_size=cfg.get("shared_expert_intermediate_size", 0) or 0,

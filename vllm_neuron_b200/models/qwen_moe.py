@@ -27,6 +27,8 @@ class MoEMixin:
 
     route_mode = M.ROUTE_SOFTMAX_TOPK
     expert_act = M.ACT_SILU
+    shared_gated = True   # shared expert scaled by sigmoid(x . gate) (router row E)
+    routed_scale = 1.0    # multiplies the routing weights
 
     def _init_moe(self, cfg, tp):
         W = tp.world if tp is not None else 1
@@ -46,7 +48,7 @@ class MoEMixin:
                                                 self.I_moe, self.device, shared_inter=self.I_sh)
 
     def _moe_params(self, m, p):
-        m.router = p(self.E + (1 if self.I_sh else 0), self.H)
+        m.router = p(self.E + (1 if self.I_sh and self.shared_gated else 0), self.H)
         m.w_gu = p(self.e_local, 2 * self.I_moe, self.H)
         m.w_down = p(self.e_local, self.H, self.I_moe)
         if self.I_sh:
@@ -58,8 +60,10 @@ class MoEMixin:
     def _moe_mlp(self, ly, x, res, nxt_norm, T):
         h = self.ws_h[:T]
         M.moe_block(x, ly.router, ly.w_gu, ly.w_down, self.topk, self.route_mode, self.renorm,
-                    act=self.expert_act, e_start=self.e_start, ws=self.moe_ws, out=h,
-                    num_experts=self.E, shared_gu=ly.sh_gu, shared_down=ly.sh_down)
+                    router_b=getattr(ly, "router_bias", None), act=self.expert_act,
+                    e_start=self.e_start, ws=self.moe_ws, out=h, num_experts=self.E,
+                    shared_gu=ly.sh_gu, shared_down=ly.sh_down, routed_scale=self.routed_scale,
+                    shared_gated=self.shared_gated)
         self._reduce_norm(h, res, nxt_norm, x)
 
 
@@ -95,9 +99,11 @@ def load_moe_mlp(model, ly, get_tensor, names: set[str], p: str):
     W, r = model.tp.world, model.tp.rank
     e0, el = model.e_start, model.e_local
     router = get_tensor(p + "mlp.gate.weight")
-    if model.I_sh:
+    if model.I_sh and model.shared_gated:
         router = torch.cat([router, get_tensor(p + "mlp.shared_expert_gate.weight").reshape(1, -1)], 0)
     _copy(ly.router, router, p + "router")
+    if getattr(ly, "router_bias", None) is not None:  # selection-only correction bias (GLM-4.5)
+        _copy(ly.router_bias, get_tensor(p + "mlp.gate.e_score_correction_bias").float(), p + "router_bias")
     fused = p + "mlp.experts.gate_up_proj"
     if fused in names:
         gu = get_tensor(fused)[e0:e0 + el]
@@ -110,8 +116,9 @@ def load_moe_mlp(model, ly, get_tensor, names: set[str], p: str):
     _copy(ly.w_gu, gu, p + "w_gu")
     _copy(ly.w_down, dn, p + "w_down")
     if model.I_sh:
-        g = shard_rows(get_tensor(p + "mlp.shared_expert.gate_proj.weight"), W, r)
-        u = shard_rows(get_tensor(p + "mlp.shared_expert.up_proj.weight"), W, r)
-        _copy(ly.sh_gu, torch.cat([g, u], 0), p + "shared_expert.gate_up")
-        _copy(ly.sh_down, shard_cols(get_tensor(p + "mlp.shared_expert.down_proj.weight"), W, r),
-              p + "shared_expert.down")
+        sp = p + ("mlp.shared_experts." if p + "mlp.shared_experts.gate_proj.weight" in names
+                  else "mlp.shared_expert.")
+        g = shard_rows(get_tensor(sp + "gate_proj.weight"), W, r)
+        u = shard_rows(get_tensor(sp + "up_proj.weight"), W, r)
+        _copy(ly.sh_gu, torch.cat([g, u], 0), sp + "gate_up")
+        _copy(ly.sh_down, shard_cols(get_tensor(sp + "down_proj.weight"), W, r), sp + "down")

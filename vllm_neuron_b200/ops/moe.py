@@ -33,6 +33,7 @@ from ._ext import ext
 ROUTE_TOPK_SOFTMAX = 0
 ROUTE_SOFTMAX_TOPK = 1
 ROUTE_SIGMOID_TOPK = 2
+ROUTE_SIGMOID_BIAS_TOPK = 3  # rank by sigmoid + correction bias, weigh by the plain sigmoid
 ACT_SILU = 0
 ACT_GPTOSS = 1
 EPI_BF16 = 0
@@ -89,13 +90,21 @@ class MoEWorkspace:
 
 # ------------------------------------------------------------------------------ oracles
 def route_ref(logits: torch.Tensor, k: int, mode: int, renorm: bool = True,
-              bias: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+              bias: torch.Tensor | None = None, scale: float = 1.0) -> tuple[torch.Tensor, torch.Tensor]:
     s = logits.float()
+    if mode == ROUTE_SIGMOID_BIAS_TOPK:
+        p = torch.sigmoid(s)
+        key = p + bias.float() if bias is not None else p
+        i = torch.topk(key, k, dim=-1).indices
+        v = p.gather(1, i)
+        if renorm:
+            v = v / (v.sum(-1, keepdim=True) + 1e-20)
+        return i.to(torch.int32), v * scale
     if bias is not None:
         s = s + bias.float()
     if mode == ROUTE_TOPK_SOFTMAX:
         v, i = torch.topk(s, k, dim=-1)
-        return i.to(torch.int32), torch.softmax(v, dim=-1)
+        return i.to(torch.int32), torch.softmax(v, dim=-1) * scale
     if mode == ROUTE_SOFTMAX_TOPK:
         s = torch.softmax(s, dim=-1)
     else:
@@ -103,7 +112,7 @@ def route_ref(logits: torch.Tensor, k: int, mode: int, renorm: bool = True,
     v, i = torch.topk(s, k, dim=-1)
     if renorm:
         v = v / v.sum(-1, keepdim=True)
-    return i.to(torch.int32), v
+    return i.to(torch.int32), v * scale
 
 
 def experts_ref(x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, w_gu: torch.Tensor,
@@ -141,13 +150,14 @@ def experts_ref(x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, w_gu: torch
 def route(logits: torch.Tensor, k: int, mode: int, renorm: bool = True,
           bias: torch.Tensor | None = None, ids: torch.Tensor | None = None,
           weights: torch.Tensor | None = None, num_experts: int | None = None,
-          shared_gate: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+          shared_gate: torch.Tensor | None = None, scale: float = 1.0) -> tuple[torch.Tensor, torch.Tensor]:
     """Top-k routing of ``logits [T, E]``.  With ``num_experts = E`` and ``logits [T, E + 1]``
-    the last column is a shared expert's gate logit and ``shared_gate[t]`` receives its sigmoid."""
+    the last column is a shared expert's gate logit and ``shared_gate[t]`` receives its sigmoid.
+    The weights are multiplied by ``scale`` (routed scaling factor)."""
     T = logits.shape[0]
     E = num_experts or logits.shape[1]
     if not logits.is_cuda:
-        i, v = route_ref(logits[:, :E], k, mode, renorm, bias)
+        i, v = route_ref(logits[:, :E], k, mode, renorm, bias, scale)
         if shared_gate is not None:
             shared_gate[:T].copy_(torch.sigmoid(logits[:, E].float()))
         if ids is not None:
@@ -160,7 +170,7 @@ def route(logits: torch.Tensor, k: int, mode: int, renorm: bool = True,
         weights = torch.empty(T, k, dtype=torch.float32, device=logits.device)
     ids, weights = ids[:T], weights[:T]
     ext().moe_route(logits, bias, E, k, mode, renorm, ids, weights,
-                    shared_gate[:T] if shared_gate is not None else None)
+                    shared_gate[:T] if shared_gate is not None else None, float(scale))
     return ids, weights
 
 
@@ -206,14 +216,17 @@ def moe_block(x: torch.Tensor, router_w: torch.Tensor, w_gu: torch.Tensor, w_dow
               ws: MoEWorkspace | None = None, out: torch.Tensor | None = None,
               num_experts: int | None = None, shared_gu: torch.Tensor | None = None,
               shared_down: torch.Tensor | None = None, fp4_gu: torch.Tensor | None = None,
-              fp4_down: torch.Tensor | None = None, fp4_max_tokens: int = 64) -> torch.Tensor:
+              fp4_down: torch.Tensor | None = None, fp4_max_tokens: int = 64,
+              routed_scale: float = 1.0, shared_gated: bool = True) -> torch.Tensor:
     """Routed experts for ``x [T, H]`` (see the module docstring); returns ``out [T, H]`` bf16.
 
     ``w_gu [e_local, 2I, H]`` holds each expert's gate rows followed by its up rows,
     ``w_down [e_local, H, I]``; biases are bf16 ``[e_local, 2I]`` / ``[e_local, H]`` and the
     router bias fp32 ``[E]``.  With a shared expert (``shared_gu [2Is, H]`` gate rows then up
     rows, ``shared_down [H, Is]``) ``router_w`` has ``E + 1`` rows, the last being the shared
-    expert's gate, and ``out += sigmoid(x . gate) * shared_expert(x)``.
+    expert's gate, and ``out += sigmoid(x . gate) * shared_expert(x)``; with
+    ``shared_gated=False`` the router has ``E`` rows and ``out += shared_expert(x)``.
+    ``routed_scale`` multiplies the routing weights (GLM-4.5's routed scaling factor).
     """
     T, H = x.shape
     e_local, I2, _ = w_gu.shape
@@ -224,10 +237,11 @@ def moe_block(x: torch.Tensor, router_w: torch.Tensor, w_gu: torch.Tensor, w_dow
         out = torch.empty(T, H, dtype=torch.bfloat16, device=x.device)
     if not x.is_cuda:
         logits = (x.float() @ router_w.float().t()).to(x.dtype)
-        ids, w = route_ref(logits[:, :E], k, mode, renorm, router_b)
+        ids, w = route_ref(logits[:, :E], k, mode, renorm, router_b, routed_scale)
         r = experts_ref(x, ids, w, w_gu, w_down, b_gu, b_down, act, alpha, limit, e_start)
         if has_shared:
-            r = r + torch.sigmoid(logits[:, E:E + 1].float()) * shared_expert_ref(x, shared_gu, shared_down)
+            gate = torch.sigmoid(logits[:, E:E + 1].float()) if shared_gated else 1.0
+            r = r + gate * shared_expert_ref(x, shared_gu, shared_down)
         out.copy_(r.to(out.dtype))
         return out
     if T == 0:
@@ -240,8 +254,9 @@ def moe_block(x: torch.Tensor, router_w: torch.Tensor, w_gu: torch.Tensor, w_dow
         L.gemm_skinny_bf16(x, router_w, out=logits)
     else:
         L.gemm_out(x, router_w, out=logits)
+    gated = has_shared and shared_gated
     ids, w = route(logits, k, mode, renorm, router_b, ws.ids, ws.weights, E,
-                   ws.shared_gate if has_shared else None)
+                   ws.shared_gate if gated else None, routed_scale)
     shared = None
     if has_shared:
         from .activation import silu_mul
@@ -270,5 +285,5 @@ def moe_block(x: torch.Tensor, router_w: torch.Tensor, w_gu: torch.Tensor, w_dow
     else:
         ext().gemm_grouped(a, w_down, y, ws.gtiles, ws.gcount, EPI_BF16, 256 if H % 256 == 0 else 128)
     ext().moe_combine(y, ws.inv_pos[:R], w, ids, b_down, e_start, shared,
-                      ws.shared_gate[:T] if has_shared else None, out)
+                      ws.shared_gate[:T] if gated else None, out)
     return out

@@ -85,11 +85,7 @@ def load_dense_decoder(model, get_tensor: Callable[[str], torch.Tensor], names: 
         if mlp_loader is not None:
             mlp_loader(model, ly, get_tensor, names, p)
             continue
-        g = shard_rows(get_tensor(p + "mlp.gate_proj.weight"), W, r)
-        u = shard_rows(get_tensor(p + "mlp.up_proj.weight"), W, r)
-        gu = L.interleave_gate_up(g, u) if model.silu_blk else torch.cat([g, u], 0)
-        _copy(ly.gate_up, gu, p + "gate_up")
-        _copy(ly.down, shard_cols(get_tensor(p + "mlp.down_proj.weight"), W, r), p + "down_proj")
+        load_dense_mlp(model, ly, get_tensor, p)
     _copy(model.final_norm, get_tensor(pre + "norm.weight"), "norm")
     if not cfg.tie_word_embeddings:
         head = "lm_head.weight"
@@ -97,6 +93,17 @@ def load_dense_decoder(model, get_tensor: Callable[[str], torch.Tensor], names: 
             _copy(model.lm_head, shard_rows(get_tensor(head), W, r, model.V_local), "lm_head")
         else:  # encoder-only checkpoints (embedding models) carry no LM head
             model.lm_head = model.embed
+
+
+def load_dense_mlp(model, ly, get_tensor, p: str):
+    """SwiGLU MLP of one layer: gate/up rows sharded (and block-interleaved for the fused SiLU
+    epilogue), down columns sharded."""
+    W, r = model.tp.world, model.tp.rank
+    g = shard_rows(get_tensor(p + "mlp.gate_proj.weight"), W, r)
+    u = shard_rows(get_tensor(p + "mlp.up_proj.weight"), W, r)
+    gu = L.interleave_gate_up(g, u) if model.silu_blk else torch.cat([g, u], 0)
+    _copy(ly.gate_up, gu, p + "gate_up")
+    _copy(ly.down, shard_cols(get_tensor(p + "mlp.down_proj.weight"), W, r), p + "down_proj")
 
 
 def _expert_tensor(get_tensor, names, base: str) -> torch.Tensor:
