@@ -535,8 +535,7 @@ void gated_delta_rule(const at::Tensor& qkv, const at::Tensor& z, const at::Tens
   TORCH_CHECK(z.stride(0) == a.stride(0) && z.stride(0) == b.stride(0), "z, a, b must share a row stride");
   const c10::cuda::CUDAGuard guard(qkv.device());
   b200::GatedDeltaParams p{};
-  // q and k are l2-normalised in place: qkv is the conv output scratch of this layer
-  p.qkv = reinterpret_cast<__nv_bfloat16*>(qkv.data_ptr());
+  p.qkv = reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr());
   p.ld_qkv = qkv.stride(0);
   p.z = reinterpret_cast<const __nv_bfloat16*>(z.data_ptr());
   p.a = reinterpret_cast<const __nv_bfloat16*>(a.data_ptr());
@@ -555,8 +554,8 @@ void gated_delta_rule(const at::Tensor& qkv, const at::Tensor& z, const at::Tens
   p.dk = (int)state.size(2);
   p.dv = (int)state.size(3);
   p.T = (int)out.size(0);
-  at::Tensor gb = at::empty({std::max<int64_t>(p.T, 1), Hv, 2}, qkv.options().dtype(at::kFloat));
-  p.gb = reinterpret_cast<float2*>(gb.data_ptr<float>());
+  at::Tensor gb = at::empty({std::max<int64_t>(p.T, 1), Hv, 4}, qkv.options().dtype(at::kFloat));
+  p.gb = reinterpret_cast<float4*>(gb.data_ptr<float>());
   b200::gated_delta_rule_launch(p, linear_batch(q_start, seq_lens, slots), cur_stream());
   // normalisation / gates pass, recurrence, gated RMSNorm
   check_launch("gated_delta_rule", seq_lens.size(0) > 0 ? (p.T > 0 ? 3 : 1) : 0);

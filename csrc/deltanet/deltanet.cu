@@ -13,7 +13,7 @@
 //
 //   causal_conv1d      one thread per channel, a sliding window of K - 1 inputs in registers,
 //                      loads of the step's tokens unrolled so they are in flight together.
-//   gated_delta_rule   a per-token pass normalises q, k in place and computes the gates; then
+//   gated_delta_rule   a per-token pass computes the q / k inverse norms and the gates; then
 //                      per (sequence, value head, 32 value columns) one CTA of 4 warps; a warp
 //                      keeps 8 columns of S in registers (16 rows x 2 columns per lane) and
 //                      reduces over dk with shuffles, so tokens are processed in order (the
@@ -77,30 +77,33 @@ __global__ void __launch_bounds__(128) causal_conv1d_kernel(
   for (int j = 0; j < K - 1; ++j) st[j] = __float2bfloat16(win[j]);
 }
 
-// Per token: q and k of every key head l2-normalised in place (bf16, as the reference computes
-// the norm in the activation dtype), and the decay / write strength of every value head,
-// gb[t, h] = (g, beta) with g = exp(-exp(A_log) * softplus(a + dt_bias)), beta = sigmoid(b).
-// Hoisting these out of the recurrence removes work every value column used to repeat.
+// Per token: the inverse l2 norms of q and k of every key head and the decay / write strength
+// of every value head, packed per value head as gb[t, h] = (g, beta, 1/|q|, 1/|k|) with
+// g = exp(-exp(A_log) * softplus(a + dt_bias)) and beta = sigmoid(b).  Hoisting these out of
+// the recurrence removes the reductions every value column used to repeat; q and k stay
+// unmodified (the recurrence applies the fp32 factors).
 __global__ void __launch_bounds__(256) gdn_prepare_kernel(const GatedDeltaParams p) {
   pdl_trigger();
   pdl_wait();
+  __shared__ float inv_norm[2 * 64];  // q heads then k heads (Hk <= 64)
   const long long t = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __nv_bfloat16* row = p.qkv + t * p.ld_qkv;
-  for (int h = warp; h < 2 * p.Hk; h += blockDim.x >> 5) {  // q heads then k heads
-    uint2* ptr = reinterpret_cast<uint2*>(row + (long long)h * 128 + lane * 4);
-    const uint2 u = *ptr;
+  const __nv_bfloat16* row = p.qkv + t * p.ld_qkv;
+  for (int h = warp; h < 2 * p.Hk; h += blockDim.x >> 5) {
+    const uint2 u = *reinterpret_cast<const uint2*>(row + (long long)h * 128 + lane * 4);
     const float2 f0 = unpack_bf16x2(u.x), f1 = unpack_bf16x2(u.y);
     float ss = f0.x * f0.x + f0.y * f0.y + f1.x * f1.x + f1.y * f1.y;
     ss = warp_sum(ss);
-    const float inv = rsqrtf(ss + 1e-6f);
-    *ptr = make_uint2(pack_bf16x2(f0.x * inv, f0.y * inv), pack_bf16x2(f1.x * inv, f1.y * inv));
+    if (lane == 0) inv_norm[h] = rsqrtf(ss + 1e-6f);
   }
+  __syncthreads();
+  const int rep = p.Hv / p.Hk;
   for (int h = threadIdx.x; h < p.Hv; h += blockDim.x) {
     const float a = __bfloat162float(p.a[t * p.ld_zab + h]);
     const float bb = __bfloat162float(p.b[t * p.ld_zab + h]);
     const float g = __expf(-__expf(p.A_log[h]) * softplus_d(a + p.dt_bias[h]));
-    p.gb[t * p.Hv + h] = make_float2(g, 1.f / (1.f + __expf(-bb)));
+    const int kh = h / rep;
+    p.gb[t * p.Hv + h] = make_float4(g, 1.f / (1.f + __expf(-bb)), inv_norm[kh], inv_norm[p.Hk + kh]);
   }
 }
 
@@ -145,7 +148,7 @@ __global__ void __launch_bounds__(128) gated_delta_rule_kernel(const GatedDeltaP
 
   uint4 nq[2], nk[2];
   uint32_t nv = 0;
-  float2 ngb = make_float2(0.f, 0.f);
+  float4 ngb = make_float4(0.f, 0.f, 0.f, 0.f);
   auto load = [&](long long t) {
     const uint4* q4 = reinterpret_cast<const uint4*>(p.qkv + t * p.ld_qkv + q_off);
     const uint4* k4 = reinterpret_cast<const uint4*>(p.qkv + t * p.ld_qkv + k_off);
@@ -174,8 +177,10 @@ __global__ void __launch_bounds__(128) gated_delta_rule_kernel(const GatedDeltaP
       }
     }
     const float2 vt = unpack_bf16x2(nv);
-    const float g = ngb.x, beta = ngb.y;
+    const float g = ngb.x, beta = ngb.y, iq = ngb.z * qscale, ik = ngb.w;
     if (i + 1 < n) load(t + 1);
+#pragma unroll
+    for (int r = 0; r < R; ++r) k[r] *= ik;
     // kv = (g S)^T k for both columns
     float kv0 = 0.f, kv1 = 0.f;
 #pragma unroll
@@ -204,7 +209,7 @@ __global__ void __launch_bounds__(128) gated_delta_rule_kernel(const GatedDeltaP
     }
     if (kg == 0)
       *reinterpret_cast<uint32_t*>(p.out + t * p.ld_out + (long long)h * DV + v0) =
-          pack_bf16x2(o0 * qscale, o1 * qscale);
+          pack_bf16x2(o0 * iq, o1 * iq);
   }
 #pragma unroll
   for (int r = 0; r < R; ++r)
@@ -282,6 +287,7 @@ void gated_delta_rule_launch(const GatedDeltaParams& p, const LinearAttnBatch& b
   if (p.ld_qkv % 8 != 0 || p.ld_zab % 4 != 0 || p.ld_out % 4 != 0)
     throw std::invalid_argument("gated_delta_rule: row strides must allow vector loads");
   if (b.B == 0) return;
+  if (p.Hk > 64) throw std::invalid_argument("gated_delta_rule: at most 64 key heads per rank");
   if (p.T > 0) launch_pdl(gdn_prepare_kernel, dim3(p.T), dim3(256), 0, s, p);
   constexpr int cols_per_cta = kGdnWarps * kGdnColsPerWarp;
   launch_pdl(gated_delta_rule_kernel, dim3(b.B, p.Hv, 128 / cols_per_cta), dim3(32 * kGdnWarps), 0,

@@ -26,8 +26,7 @@ void causal_conv1d_launch(const __nv_bfloat16* x, long long ldx, int C, const __
                           cudaStream_t s);
 
 struct GatedDeltaParams {
-  __nv_bfloat16* qkv;         // conv output [T, 2 * Hk * dk + Hv * dv]: q | k | v (q, k are
-                              // l2-normalised in place)
+  const __nv_bfloat16* qkv;   // conv output [T, 2 * Hk * dk + Hv * dv]: q | k | v
   long long ld_qkv;
   const __nv_bfloat16* z;     // output gate [T, Hv * dv]
   const __nv_bfloat16* a;     // decay input [T, Hv]
@@ -42,7 +41,7 @@ struct GatedDeltaParams {
   __nv_bfloat16* out;         // [T, Hv * dv]
   long long ld_out;
   int Hk, Hv, dk, dv;
-  float2* gb;                 // scratch [T, Hv]: (decay g, write strength beta) per token, head
+  float4* gb;                 // scratch [T, Hv]: (g, beta, 1/|q|, 1/|k|) per token and value head
   int T;                      // tokens of this step (rows of out)
 };
 

@@ -63,13 +63,11 @@ def test_gated_delta_rule(cuda_device, Hk, Hv):
     st_ref = state.cpu().clone()
     out = torch.empty(T, Hv * dv, device=cuda_device, dtype=torch.bfloat16)
     for _ in range(2):  # the second call continues from the updated state
-        qkv_in = qkv.cpu()  # the kernel normalises q, k of its (scratch) input in place
         DN.gated_delta_rule(qkv, z, a, b, A_log, dt_bias, nw, 1e-6, qs, sl, slots, state, out, Hk, Hv)
-        ref = DN.gated_delta_rule_ref(qkv_in, z.cpu(), a.cpu(), b.cpu(), A_log.cpu(), dt_bias.cpu(),
+        ref = DN.gated_delta_rule_ref(qkv.cpu(), z.cpu(), a.cpu(), b.cpu(), A_log.cpu(), dt_bias.cpu(),
                                       nw.cpu(), 1e-6, qs.cpu(), sl.cpu(), slots.cpu(), st_ref, Hk, Hv)
         assert _rel_err(out.cpu(), ref) < 2e-2
-        # q, k are normalised in bf16 (the activation dtype) by the kernel, in fp32 by the oracle
-        assert _rel_err(state.cpu(), st_ref) < 5e-3
+        assert _rel_err(state.cpu(), st_ref) < 1e-3
         sl = sl + torch.tensor(q_lens, dtype=torch.int32, device=cuda_device)
 
 

@@ -47,8 +47,7 @@ def gated_delta_rule(qkv: torch.Tensor, z: torch.Tensor, a: torch.Tensor, b: tor
                      q_start: torch.Tensor, seq_lens: torch.Tensor, slots: torch.Tensor,
                      state: torch.Tensor, out: torch.Tensor, Hk: int, Hv: int) -> torch.Tensor:
     """Recurrent gated delta rule + gated RMSNorm; ``qkv [T, 2 Hk dk + Hv dv]``,
-    ``z [T, Hv dv]``, ``a, b [T, Hv]`` -> ``out [T, Hv dv]``; updates ``state``.  On the GPU
-    the q and k columns of ``qkv`` are l2-normalised in place (it is the conv scratch)."""
+    ``z [T, Hv dv]``, ``a, b [T, Hv]`` -> ``out [T, Hv dv]``; updates ``state``."""
     if not qkv.is_cuda:
         out.copy_(gated_delta_rule_ref(qkv, z, a, b, A_log, dt_bias, norm_w, eps, q_start, seq_lens,
                                        slots, state, Hk, Hv).to(out.dtype))
@@ -69,11 +68,8 @@ def gated_delta_rule_ref(qkv, z, a, b, A_log, dt_bias, norm_w, eps, q_start, seq
     rep = Hv // Hk
     q = q.repeat_interleave(rep, 1)
     k = k.repeat_interleave(rep, 1)
-    q = q * torch.rsqrt((q * q).sum(-1, keepdim=True) + 1e-6)
+    q = q * torch.rsqrt((q * q).sum(-1, keepdim=True) + 1e-6) * dk ** -0.5
     k = k * torch.rsqrt((k * k).sum(-1, keepdim=True) + 1e-6)
-    if qkv.dtype == torch.bfloat16:  # normalised in the activation dtype (as the kernel and HF)
-        q, k = q.to(torch.bfloat16).float(), k.to(torch.bfloat16).float()
-    q = q * dk ** -0.5
     g = torch.exp(-A_log.float().exp() * F.softplus(a.float() + dt_bias.float()))   # [T, Hv]
     beta = torch.sigmoid(b.float())
     o = torch.zeros(T, Hv, dv)
