@@ -191,7 +191,8 @@ void rope_kv_write(at::Tensor& qkv, const at::Tensor& positions,
                    c10::optional<at::Tensor> v_cache, c10::optional<at::Tensor> q_norm_w,
                    c10::optional<at::Tensor> k_norm_w, double eps, int64_t num_q_heads,
                    int64_t num_kv_heads, int64_t head_dim, int64_t rot_dim, bool neox,
-                   bool clear_input, double q_pos_beta, double q_pos_period) {
+                   bool clear_input, double q_pos_beta, double q_pos_period,
+                   c10::optional<at::Tensor> qkv_bias) {
   CHECK_CUDA(qkv);
   TORCH_CHECK(q_pos_beta == 0.0 || q_pos_period > 0.0, "rope_kv_write: q_pos_period must be positive");
   const c10::cuda::CUDAGuard guard(qkv.device());
@@ -222,6 +223,12 @@ void rope_kv_write(at::Tensor& qkv, const at::Tensor& positions,
   p.rot_dim = (int)rot_dim;
   p.neox = neox;
   p.clear_input = clear_input;
+  if (qkv_bias.has_value()) {
+    TORCH_CHECK(qkv_bias->scalar_type() == at::kFloat && qkv_bias->is_contiguous() &&
+                    qkv_bias->numel() == (num_q_heads + 2 * num_kv_heads) * head_dim,
+                "rope_kv_write: qkv_bias must be fp32 [(Hq + 2 Hkv) * D]");
+    p.qkv_bias = qkv_bias->data_ptr<float>();
+  }
   p.q_pos_beta = (float)q_pos_beta;
   p.q_pos_period = (float)(q_pos_period > 0.0 ? q_pos_period : 1.0);
   b200::rope_kv_write_launch(p, qkv.data_ptr(), qkv.scalar_type() == at::kFloat,

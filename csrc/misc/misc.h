@@ -27,6 +27,7 @@ struct RopeKvParams {
   int Hq, Hkv, head_dim, rot_dim, block_size;
   bool neox;
   bool clear_input;
+  const float* qkv_bias;       // [(Hq + 2 Hkv) * D] fp32 added to the input row, or null
   // q *= 1 + q_pos_beta * log(1 + floor(pos / q_pos_period)) after rotation (0: off)
   float q_pos_beta;
   float q_pos_period;

@@ -211,6 +211,10 @@ __global__ void __launch_bounds__(256) rope_kv_write_kernel(const RopeKvParams p
     float v[PER];
 #pragma unroll
     for (int e = 0; e < PER; ++e) v[e] = to_f(src[lane + 32 * e]);
+    if (p.qkv_bias != nullptr) {
+#pragma unroll
+      for (int e = 0; e < PER; ++e) v[e] += p.qkv_bias[(long long)h * D + lane + 32 * e];
+    }
     if ((is_q && p.q_norm_w) || (is_k && p.k_norm_w)) {
       float ss = 0.f;
 #pragma unroll

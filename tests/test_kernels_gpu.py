@@ -327,15 +327,17 @@ def test_bounded_peer_wait_expires_and_context_survives(cuda_device):
 
 
 def test_rope_query_position_scale(cuda_device):
-    """Long-context query temperature 1 + beta * log(1 + floor(pos / period)) in the rope kernel."""
+    """Long-context query temperature 1 + beta * log(1 + floor(pos / period)) and the fused
+    qkv bias in the rope kernel."""
     T, Hq, Hkv, D, bs, nb = 24, 4, 2, 128, 16, 4
     qkv = torch.randn(T, (Hq + 2 * Hkv) * D, device=cuda_device, dtype=torch.bfloat16)
     qkv_cpu = qkv.cpu().clone()
     pos = torch.randint(0, 4000, (T,), dtype=torch.int32, device=cuda_device)
     tab = ops.cos_sin_table(4096, D, 1e6, device=cuda_device)
     q_out = torch.empty(T, Hq * D, device=cuda_device, dtype=torch.bfloat16)
-    ops.rope_kv_write(qkv, pos, tab, Hq, Hkv, D, q_out, q_pos_scale=(0.1, 256.0))
+    bias = torch.randn((Hq + 2 * Hkv) * D, device=cuda_device) * 0.5  # fused qkv bias
+    ops.rope_kv_write(qkv, pos, tab, Hq, Hkv, D, q_out, q_pos_scale=(0.1, 256.0), qkv_bias=bias)
     q_r = torch.empty(T, Hq * D, dtype=torch.bfloat16)
-    ops.rope_kv_write_ref(qkv_cpu, pos.cpu(), tab.cpu(), Hq, Hkv, D, q_r, None, None, None, None, None,
-                          1e-6, D, True, (0.1, 256.0))
+    ops.rope_kv_write_ref(qkv_cpu.float() + bias.cpu(), pos.cpu(), tab.cpu(), Hq, Hkv, D, q_r, None, None,
+                          None, None, None, 1e-6, D, True, (0.1, 256.0))
     assert _rel_err(q_out.cpu(), q_r) < 1e-2

@@ -199,6 +199,11 @@ class LlamaForCausalLM(torch.nn.Module):
     def bind_kv_cache(self, kv_caches: list[tuple[torch.Tensor, torch.Tensor]]):
         assert len(kv_caches) == self.num_kv_layers
         self.kv_caches = kv_caches
+        for ly in self.layers:  # weights are final here: refresh the fp32 bias copies
+            for name in ("qkv_bias", "o_bias"):
+                if getattr(ly, name, None) is not None:
+                    setattr(ly, name + "_f32", None)
+                    self._f32(ly, name)
 
     def kv_cache_shape(self, num_blocks: int) -> tuple[int, ...]:
         return (num_blocks, self.Hkv, self.block_size, self.D)
@@ -223,18 +228,16 @@ class LlamaForCausalLM(torch.nn.Module):
             if small:
                 acc = self.acc_qkv[:T]
                 L.gemm_accumulate(x, ly.qkv, acc)
-                if ly.qkv_bias is not None:
-                    acc.add_(ly.qkv_bias.float())
                 ops.rope_kv_write(acc, b.positions, self.cos_sin, self.Hq, self.Hkv, self.D, q,
                                   k_cache, v_cache, b.slot_mapping, ly.q_norm, ly.k_norm, self.eps,
-                                  rot_dim=self.cfg.rot_dim, clear_input=True, q_pos_scale=self.q_pos_scale)
+                                  rot_dim=self.cfg.rot_dim, clear_input=True, q_pos_scale=self.q_pos_scale,
+                                  qkv_bias=self._f32(ly, "qkv_bias"))
             else:
                 qkv = L.gemm_out(x[:T], ly.qkv, out=self.ws_qkv[:T])
-                if ly.qkv_bias is not None:
-                    qkv.add_(ly.qkv_bias)
                 ops.rope_kv_write(qkv, b.positions, self.cos_sin, self.Hq, self.Hkv, self.D, q,
                                   k_cache, v_cache, b.slot_mapping, ly.q_norm, ly.k_norm, self.eps,
-                                  rot_dim=self.cfg.rot_dim, q_pos_scale=self.q_pos_scale)
+                                  rot_dim=self.cfg.rot_dim, q_pos_scale=self.q_pos_scale,
+                                  qkv_bias=self._f32(ly, "qkv_bias"))
             attn = self.ws_attn[:T]
             self._attention(q, attn, k_cache, v_cache, b, window=ly.window, sinks=ly.sinks)
             nxt_norm = ly.post_norm
@@ -242,7 +245,7 @@ class LlamaForCausalLM(torch.nn.Module):
                 acc = self.acc_h[:T]
                 L.gemm_accumulate(attn, ly.o, acc)
                 if ly.o_bias is not None and tp.rank == 0:
-                    acc.add_(ly.o_bias.float())
+                    acc.add_(self._f32(ly, "o_bias"))
                 self._allreduce_norm(acc, res, nxt_norm, x, fused)
             else:
                 if Tg > T:
@@ -261,6 +264,19 @@ class LlamaForCausalLM(torch.nn.Module):
         if b.want_hidden:
             return x.index_select(0, b.logits_indices.long())
         return self.compute_logits(x, b.logits_indices)
+
+    @staticmethod
+    def _f32(ly, name: str) -> torch.Tensor | None:
+        """fp32 copy of a bias parameter, cached on the layer (made at KV-cache binding, before
+        any graph capture, so the forward launches no conversion kernels)."""
+        t = getattr(ly, name, None)
+        if t is None:
+            return None
+        c = getattr(ly, name + "_f32", None)
+        if c is None or c.shape != t.shape:
+            c = t.detach().float().contiguous()
+            setattr(ly, name + "_f32", c)
+        return c
 
     def _embed(self, b: ForwardBatch, T: int, small: bool):
         """Embedding (vocab-parallel) and the first RMSNorm.  Returns ``(res, x, Tg)``: the

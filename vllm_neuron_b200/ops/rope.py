@@ -88,15 +88,18 @@ def rope_kv_write(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Ten
                   slot_mapping: torch.Tensor | None = None, q_norm_w: torch.Tensor | None = None,
                   k_norm_w: torch.Tensor | None = None, eps: float = 1e-6,
                   rot_dim: int | None = None, neox: bool = True,
-                  clear_input: bool = False, q_pos_scale: tuple[float, float] | None = None) -> torch.Tensor:
+                  clear_input: bool = False, q_pos_scale: tuple[float, float] | None = None,
+                  qkv_bias: torch.Tensor | None = None) -> torch.Tensor:
     """Rotate q/k of ``qkv [T, (Hq + 2 Hkv) * D]``; write rotated q to ``q_out [T, Hq * D]`` and
     k/v into the paged cache at ``slot_mapping`` (int32, negative = skip).  ``q_pos_scale =
     (beta, period)`` multiplies the rotated q by ``1 + beta * log(1 + floor(pos / period))``
-    (the long-context query temperature of Ministral-3 / Llama-4 configs)."""
+    (the long-context query temperature of Ministral-3 / Llama-4 configs).  ``qkv_bias`` (fp32
+    ``[(Hq + 2 Hkv) * D]``) is added to the input rows first."""
     rot_dim = rot_dim or head_dim
     beta, period = q_pos_scale if q_pos_scale else (0.0, 1.0)
     if not qkv.is_cuda:
-        rope_kv_write_ref(qkv, positions, cos_sin, num_q_heads, num_kv_heads, head_dim, q_out,
+        src = qkv if qkv_bias is None else (qkv[:, :qkv_bias.numel()].float() + qkv_bias.float())
+        rope_kv_write_ref(src, positions, cos_sin, num_q_heads, num_kv_heads, head_dim, q_out,
                           k_cache, v_cache, slot_mapping, q_norm_w, k_norm_w, eps, rot_dim, neox,
                           q_pos_scale)
         if clear_input:
@@ -104,7 +107,8 @@ def rope_kv_write(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Ten
         return q_out
     ext().rope_kv_write(qkv, positions, slot_mapping, cos_sin, q_out, k_cache, v_cache,
                         q_norm_w, k_norm_w, eps, num_q_heads, num_kv_heads, head_dim, rot_dim,
-                        neox, clear_input and qkv.dtype == torch.float32, float(beta), float(period))
+                        neox, clear_input and qkv.dtype == torch.float32, float(beta), float(period),
+                        qkv_bias)
     return q_out
 
 
