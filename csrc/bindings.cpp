@@ -421,6 +421,34 @@ void moe_route(const at::Tensor& logits, c10::optional<at::Tensor> bias, int64_t
   check_launch("moe_route", logits.size(0) > 0 ? 1 : 0);
 }
 
+// Fused router GEMV + top-k for decode batches: x [T, H], w [rows, H] (rows = E, or E + 1 with
+// the shared-expert gate row), logits [T, >= rows] bf16 output.
+void moe_router_topk(const at::Tensor& x, const at::Tensor& w, c10::optional<at::Tensor> bias,
+                     int64_t num_experts, int64_t k, int64_t mode, bool renorm, double scale,
+                     at::Tensor& logits, at::Tensor& ids, at::Tensor& weights,
+                     c10::optional<at::Tensor> shared_gate) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  CHECK_BF16(w);
+  CHECK_BF16(logits);
+  TORCH_CHECK(x.stride(1) == 1 && w.is_contiguous() && logits.stride(1) == 1, "moe_router_topk: layouts");
+  TORCH_CHECK(ids.scalar_type() == at::kInt && weights.scalar_type() == at::kFloat, "moe_router_topk: out dtypes");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const float* b = nullptr;
+  if (bias.has_value()) {
+    TORCH_CHECK(bias->scalar_type() == at::kFloat, "moe_router_topk: bias must be fp32");
+    b = bias->data_ptr<float>();
+  }
+  b200::moe_router_topk_launch(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0),
+                               reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), (int)w.size(0),
+                               (int)x.size(1), b, (int)x.size(0), (int)num_experts, (int)k, (int)mode,
+                               renorm, (float)scale, reinterpret_cast<__nv_bfloat16*>(logits.data_ptr()),
+                               logits.stride(0), ids.data_ptr<int>(), weights.data_ptr<float>(),
+                               shared_gate.has_value() ? shared_gate->data_ptr<float>() : nullptr,
+                               cur_stream());
+  check_launch("moe_router_topk", x.size(0) > 0 ? 1 : 0);
+}
+
 void moe_align(const at::Tensor& ids, int64_t e_start, int64_t e_local, at::Tensor& offsets,
                at::Tensor& sorted_src, at::Tensor& row_expert, at::Tensor& inv_pos,
                at::Tensor& gtiles, at::Tensor& gcount) {
@@ -655,6 +683,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_grouped", &gemm_grouped);
   m.def("moe_route", &moe_route);
   m.def("moe_align", &moe_align);
+  m.def("moe_router_topk", &moe_router_topk);
   m.def("moe_gather", &moe_gather);
   m.def("moe_act", &moe_act);
   m.def("moe_combine", &moe_combine);

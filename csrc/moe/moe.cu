@@ -5,7 +5,8 @@
 //
 //   route    one warp per token: scores from the router logits (+ bias), top-k selection by k
 //            rounds of warp arg-max, weights by softmax / sigmoid (reference orderings:
-//            vllm_neuron/functional/moe/router.py:19-71, GPT-OSS top-k then softmax).
+//            vllm_neuron/functional/moe/router.py:19-71, GPT-OSS top-k then softmax); for
+//            decode batches fused with the router GEMV (moe_router_topk).
 //   align    one CTA: per-expert histogram, exclusive scan, 128-row tile list per expert and
 //            the scatter of assignments into expert-contiguous rows (reference semantics:
 //            build_blockwise_mapping, vllm_neuron/functional/moe/moe_blockwise.py:27 and
@@ -18,6 +19,7 @@
 //            shared is the optional shared expert, g its sigmoid gate from the router).
 #include <cuda_bf16.h>
 
+#include <atomic>
 #include <stdexcept>
 
 #include "../common.cuh"
@@ -29,19 +31,16 @@ namespace {
 constexpr int kMaxExpertsPerLane = 16;  // E <= 512
 }
 
-__global__ void moe_route_kernel(const __nv_bfloat16* __restrict__ logits, long long ld,
-                                 const float* __restrict__ bias, int T, int E, int k, int mode,
-                                 int renorm, int* __restrict__ ids, float* __restrict__ weights,
-                                 float* __restrict__ shared_gate, float scale) {
-  pdl_trigger();
-  pdl_wait();
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+// Routing of one token by one warp.  `logit(e)` returns the router logit of expert e (and of
+// the shared expert's gate at e = E); the token's k choices go to ids_row / w_row.
+template <typename LogitFn>
+__device__ __forceinline__ void route_row(LogitFn logit, const float* __restrict__ bias, int E,
+                                          int k, int mode, int renorm, float scale,
+                                          int* __restrict__ ids_row, float* __restrict__ w_row,
+                                          float* __restrict__ shared_gate_out) {
   const int lane = threadIdx.x & 31;
-  if (warp >= T) return;
-  const __nv_bfloat16* row = logits + (long long)warp * ld;
   // column E (when present) is the shared expert's gate logit
-  if (shared_gate != nullptr && lane == 0)
-    shared_gate[warp] = 1.f / (1.f + __expf(-__bfloat162float(row[E])));
+  if (shared_gate_out != nullptr && lane == 0) *shared_gate_out = 1.f / (1.f + __expf(-logit(E)));
   const bool bias_after = mode == ROUTE_SIGMOID_BIAS_TOPK;  // bias only ranks the experts
   float v[kMaxExpertsPerLane], raw[kMaxExpertsPerLane];
 #pragma unroll
@@ -49,7 +48,7 @@ __global__ void moe_route_kernel(const __nv_bfloat16* __restrict__ logits, long 
     const int e = i * 32 + lane;
     float x = -INFINITY;
     if (e < E) {
-      x = __bfloat162float(row[e]);
+      x = logit(e);
       if (bias != nullptr && !bias_after) x += bias[e];
     }
     v[i] = x;
@@ -136,9 +135,79 @@ __global__ void moe_route_kernel(const __nv_bfloat16* __restrict__ logits, long 
     }
   }
   if (lane < k) {
-    ids[(long long)warp * k + lane] = sel_e;
-    weights[(long long)warp * k + lane] = w * scale;
+    ids_row[lane] = sel_e;
+    w_row[lane] = w * scale;
   }
+}
+
+__global__ void moe_route_kernel(const __nv_bfloat16* __restrict__ logits, long long ld,
+                                 const float* __restrict__ bias, int T, int E, int k, int mode,
+                                 int renorm, int* __restrict__ ids, float* __restrict__ weights,
+                                 float* __restrict__ shared_gate, float scale) {
+  pdl_trigger();
+  pdl_wait();
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (warp >= T) return;
+  const __nv_bfloat16* row = logits + (long long)warp * ld;
+  route_row([&](int e) { return __bfloat162float(row[e]); }, bias, E, k, mode, renorm, scale,
+            ids + (long long)warp * k, weights + (long long)warp * k,
+            shared_gate != nullptr ? shared_gate + warp : nullptr);
+}
+
+// Decode-sized batches: router GEMV and top-k in one kernel.  One CTA per token: the token's
+// row sits in shared memory (fp32), each warp computes the logits of every 8th router row
+// (uint4 loads of the bf16 weights, warp reduction) rounded to bf16 as the GEMM path stores
+// them (written to `logits` too), then warp 0 routes the token.  Counterpart of the
+// reference's fused decode router (rmsnorm_router_topk_tkg,
+// vllm_neuron/functional/moe/rmsnorm_router_topk_tkg.py:34) minus the norm, which this
+// framework already fuses into the preceding all-reduce.
+__global__ void __launch_bounds__(256, 1) moe_router_topk_kernel(
+    const __nv_bfloat16* __restrict__ x, long long ldx, const __nv_bfloat16* __restrict__ w,
+    int rows, int H, const float* __restrict__ bias, int E, int k, int mode, int renorm,
+    float scale, __nv_bfloat16* __restrict__ logits, long long ldl, int* __restrict__ ids,
+    float* __restrict__ weights, float* __restrict__ shared_gate) {
+  pdl_trigger();
+  pdl_wait();
+  extern __shared__ float sm_router[];
+  float* xs = sm_router;          // [H]
+  float* lg = sm_router + H;      // [rows]
+  const int t = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const __nv_bfloat16* xr = x + (long long)t * ldx;
+  for (int i = threadIdx.x * 8; i < H; i += blockDim.x * 8) {
+    const uint4 u = *reinterpret_cast<const uint4*>(xr + i);
+    const uint32_t ws_[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 f = unpack_bf16x2(ws_[q]);
+      xs[i + 2 * q] = f.x;
+      xs[i + 2 * q + 1] = f.y;
+    }
+  }
+  __syncthreads();
+  for (int e = warp; e < rows; e += blockDim.x >> 5) {
+    const __nv_bfloat16* wr = w + (long long)e * H;
+    float acc = 0.f;
+    for (int i = lane * 8; i < H; i += 32 * 8) {
+      const uint4 u = *reinterpret_cast<const uint4*>(wr + i);
+      const uint32_t ws_[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = unpack_bf16x2(ws_[q]);
+        acc += f.x * xs[i + 2 * q] + f.y * xs[i + 2 * q + 1];
+      }
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) {
+      const __nv_bfloat16 r = __float2bfloat16(acc);
+      lg[e] = __bfloat162float(r);
+      if (logits != nullptr) logits[(long long)t * ldl + e] = r;
+    }
+  }
+  __syncthreads();
+  if (warp == 0)
+    route_row([&](int e) { return lg[e]; }, bias, E, k, mode, renorm, scale, ids + (long long)t * k,
+              weights + (long long)t * k, shared_gate != nullptr ? shared_gate + t : nullptr);
 }
 
 __global__ void __launch_bounds__(1024) moe_align_kernel(const int* __restrict__ ids,
@@ -354,6 +423,24 @@ void moe_route_launch(const __nv_bfloat16* logits, long long ld, const float* bi
   launch_pdl(moe_route_kernel, dim3((T + warps_per_block - 1) / warps_per_block),
              dim3(32 * warps_per_block), 0, s, logits, ld, bias, T, E, k, mode, renorm ? 1 : 0, ids,
              weights, shared_gate, scale);
+}
+
+void moe_router_topk_launch(const __nv_bfloat16* x, long long ldx, const __nv_bfloat16* w, int rows,
+                            int H, const float* bias, int T, int E, int k, int mode, bool renorm,
+                            float scale, __nv_bfloat16* logits, long long ldl, int* ids,
+                            float* weights, float* shared_gate, cudaStream_t s) {
+  if (E > 32 * kMaxExpertsPerLane) throw std::invalid_argument("moe_router_topk: at most 512 experts");
+  if (k < 1 || k > 32 || k > E) throw std::invalid_argument("moe_router_topk: 1 <= k <= min(32, E)");
+  if (H % 8 != 0 || ldx % 8 != 0) throw std::invalid_argument("moe_router_topk: H must be a multiple of 8");
+  if (rows < E || (shared_gate != nullptr && rows < E + 1))
+    throw std::invalid_argument("moe_router_topk: router rows");
+  const int smem = (H + rows) * (int)sizeof(float);
+  if (smem > 200 * 1024) throw std::invalid_argument("moe_router_topk: hidden size too large");
+  if (T == 0) return;
+  static std::atomic<uint64_t> configured{0};
+  set_max_dynamic_smem_once(moe_router_topk_kernel, smem, configured);
+  launch_pdl(moe_router_topk_kernel, dim3(T), dim3(256), smem, s, x, ldx, w, rows, H, bias, E, k,
+             mode, renorm ? 1 : 0, scale, logits, ldl, ids, weights, shared_gate);
 }
 
 void moe_align_launch(const int* ids, int n_assign, int e_start, int e_local, int* offsets,

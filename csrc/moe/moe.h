@@ -28,6 +28,14 @@ void moe_route_launch(const __nv_bfloat16* logits, long long ld, const float* bi
                       float scale, cudaStream_t s);
 
 // Groups the T*k assignments by local expert [e_start, e_start + e_local).
+// Router GEMV (w [rows, H] bf16, rows = E or E + 1 with the shared-expert gate row) fused with
+// the routing of moe_route_launch, one CTA per token (decode batches).  `logits` (optional)
+// receives the bf16 logits [T, rows].
+void moe_router_topk_launch(const __nv_bfloat16* x, long long ldx, const __nv_bfloat16* w, int rows,
+                            int H, const float* bias, int T, int E, int k, int mode, bool renorm,
+                            float scale, __nv_bfloat16* logits, long long ldl, int* ids,
+                            float* weights, float* shared_gate, cudaStream_t s);
+
 void moe_align_launch(const int* ids, int n_assign, int e_start, int e_local, int* offsets,
                       int* sorted_src, int* row_expert, int* inv_pos, int* gtiles, int* gcount,
                       int gmax, cudaStream_t s);

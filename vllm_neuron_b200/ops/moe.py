@@ -175,6 +175,7 @@ def route(logits: torch.Tensor, k: int, mode: int, renorm: bool = True,
 
 
 TILE_COLS = 256
+ROUTER_FUSED_MAX_TOKENS = 64  # fused router GEMV + top-k below this batch size
 
 
 def pack_mxfp4(blocks: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
@@ -250,13 +251,19 @@ def moe_block(x: torch.Tensor, router_w: torch.Tensor, w_gu: torch.Tensor, w_dow
         ws = MoEWorkspace.create(T, k, E, e_local, H, I, x.device,
                                  shared_inter=shared_gu.shape[0] // 2 if has_shared else 0)
     logits = ws.logits[:T, :router_w.shape[0]]
-    if T <= L.SKINNY_MAX:
-        L.gemm_skinny_bf16(x, router_w, out=logits)
-    else:
-        L.gemm_out(x, router_w, out=logits)
     gated = has_shared and shared_gated
-    ids, w = route(logits, k, mode, renorm, router_b, ws.ids, ws.weights, E,
-                   ws.shared_gate if gated else None, routed_scale)
+    if T <= ROUTER_FUSED_MAX_TOKENS and H % 8 == 0:
+        # decode: router GEMV + top-k in one kernel (one CTA per token)
+        ids, w = ws.ids[:T], ws.weights[:T]
+        ext().moe_router_topk(x, router_w, router_b, E, k, mode, renorm, float(routed_scale), logits,
+                              ids, w, ws.shared_gate[:T] if gated else None)
+    else:
+        if T <= L.SKINNY_MAX:
+            L.gemm_skinny_bf16(x, router_w, out=logits)
+        else:
+            L.gemm_out(x, router_w, out=logits)
+        ids, w = route(logits, k, mode, renorm, router_b, ws.ids, ws.weights, E,
+                       ws.shared_gate if gated else None, routed_scale)
     shared = None
     if has_shared:
         from .activation import silu_mul
