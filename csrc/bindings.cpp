@@ -192,7 +192,8 @@ void rope_kv_write(at::Tensor& qkv, const at::Tensor& positions,
                    c10::optional<at::Tensor> k_norm_w, double eps, int64_t num_q_heads,
                    int64_t num_kv_heads, int64_t head_dim, int64_t rot_dim, bool neox,
                    bool clear_input, double q_pos_beta, double q_pos_period,
-                   c10::optional<at::Tensor> qkv_bias) {
+                   c10::optional<at::Tensor> qkv_bias, c10::optional<at::Tensor> positions3,
+                   int64_t mrope_h, int64_t mrope_w) {
   CHECK_CUDA(qkv);
   TORCH_CHECK(q_pos_beta == 0.0 || q_pos_period > 0.0, "rope_kv_write: q_pos_period must be positive");
   const c10::cuda::CUDAGuard guard(qkv.device());
@@ -228,6 +229,14 @@ void rope_kv_write(at::Tensor& qkv, const at::Tensor& positions,
                     qkv_bias->numel() == (num_q_heads + 2 * num_kv_heads) * head_dim,
                 "rope_kv_write: qkv_bias must be fp32 [(Hq + 2 Hkv) * D]");
     p.qkv_bias = qkv_bias->data_ptr<float>();
+  }
+  if (positions3.has_value()) {
+    TORCH_CHECK(positions3->scalar_type() == at::kInt && positions3->is_contiguous() &&
+                    positions3->dim() == 2 && positions3->size(1) == 3,
+                "rope_kv_write: positions3 must be int32 [T, 3]");
+    p.positions3 = positions3->data_ptr<int>();
+    p.mrope_h = (int)mrope_h;
+    p.mrope_w = (int)mrope_w;
   }
   p.q_pos_beta = (float)q_pos_beta;
   p.q_pos_period = (float)(q_pos_period > 0.0 ? q_pos_period : 1.0);

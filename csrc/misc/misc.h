@@ -28,6 +28,11 @@ struct RopeKvParams {
   bool neox;
   bool clear_input;
   const float* qkv_bias;       // [(Hq + 2 Hkv) * D] fp32 added to the input row, or null
+  // Interleaved multimodal RoPE (Qwen3-VL): positions3 [T, 3] (temporal, height, width); rotary
+  // frequency j uses the height position when j % 3 == 1 and j < 3 * mrope_h, the width
+  // position when j % 3 == 2 and j < 3 * mrope_w, else the temporal one.  null: 1-D positions.
+  const int* positions3;
+  int mrope_h, mrope_w;
   // q *= 1 + q_pos_beta * log(1 + floor(pos / q_pos_period)) after rotation (0: off)
   float q_pos_beta;
   float q_pos_period;

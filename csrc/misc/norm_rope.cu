@@ -234,7 +234,12 @@ __global__ void __launch_bounds__(256) rope_kv_write_kernel(const RopeKvParams p
 #pragma unroll
         for (int e = 0; e < HP; ++e) {
           const int i = lane + 32 * e;
-          const float c = cs[i], s = cs[D / 2 + i];
+          const float* ci = cs;
+          if (p.positions3 != nullptr) {
+            const int comp = (i % 3 == 1 && i < 3 * p.mrope_h) ? 1 : (i % 3 == 2 && i < 3 * p.mrope_w) ? 2 : 0;
+            ci = p.cos_sin + (long long)p.positions3[3 * t + comp] * p.rot_dim;
+          }
+          const float c = ci[i], s = ci[D / 2 + i];
           o[e] = v[e] * c - v[e + HP] * s;
           o[e + HP] = v[e + HP] * c + v[e] * s;
         }
@@ -298,6 +303,8 @@ __global__ void __launch_bounds__(256) rope_kv_write_kernel(const RopeKvParams p
 void rope_kv_write_launch(const RopeKvParams& p, void* qkv, bool qkv_is_f32, int T,
                           cudaStream_t stream) {
   if (T == 0) return;
+  if (p.positions3 != nullptr && !(p.neox && p.rot_dim == p.head_dim && p.head_dim >= 64))
+    throw std::invalid_argument("rope_kv_write: multimodal RoPE needs full-width neox rotation");
 #define B200_ROPE(D_)                                                                       \
   if (p.head_dim == D_) {                                                                   \
     if (qkv_is_f32)                                                                         \

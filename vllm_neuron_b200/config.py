@@ -95,7 +95,7 @@ class ModelArchConfig:
             partial_rotary_factor=cfg.get("partial_rotary_factor", rp.get("partial_rotary_factor", 1.0)),
             max_position_embeddings=cfg.get("max_position_embeddings", 8192),
             tie_word_embeddings=cfg.get("tie_word_embeddings", False),
-            qk_norm=(cfg.get("model_type", "") in ("qwen3", "qwen3_moe", "qwen3_next", "qwen3_vl",
+            qk_norm=(cfg.get("model_type", "") in ("qwen3", "qwen3_moe", "qwen3_next", "qwen3_vl", "qwen3_vl_text",
                                                    "qwen3_5_moe", "qwen3_5_moe_text", "qwen3_5", "qwen3_5_text")
                      or bool(cfg.get("use_qk_norm", False))),
             attention_bias=cfg.get("attention_bias", cfg.get("qkv_bias",

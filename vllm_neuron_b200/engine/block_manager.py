@@ -47,7 +47,8 @@ class BlockManager:
 
     def match_prefix(self, req) -> int:
         """Attach cached blocks for the longest cached prefix; returns #tokens covered."""
-        if not self.enable_prefix_caching or req.block_ids or getattr(req, "prompt_embeds", None) is not None:
+        if (not self.enable_prefix_caching or req.block_ids or getattr(req, "prompt_embeds", None) is not None
+                or getattr(req, "mm", None) is not None):
             return 0  # prompt-embedding requests have no token ids to hash
         toks = req.prompt_token_ids
         # Keep at least one token to compute so the request produces logits.
@@ -92,7 +93,8 @@ class BlockManager:
 
     def commit_full_blocks(self, req):
         """Register the request's newly completed full blocks in the prefix cache."""
-        if not self.enable_prefix_caching or getattr(req, "prompt_embeds", None) is not None:
+        if (not self.enable_prefix_caching or getattr(req, "prompt_embeds", None) is not None
+                or getattr(req, "mm", None) is not None):
             return
         n_full = min(req.num_computed_tokens, req.num_tokens) // self.block_size
         hs = self.req_hashes.setdefault(req.request_id, [])

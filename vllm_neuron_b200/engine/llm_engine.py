@@ -172,14 +172,14 @@ class LLMEngine:
     # ---------------------------------------------------------------- requests
     def add_request(self, prompt_token_ids: list[int], params: SamplingParams | None = None,
                     request_id: str | None = None, arrival_time: float | None = None,
-                    prompt_embeds: torch.Tensor | None = None) -> str:
+                    prompt_embeds: torch.Tensor | None = None, mm=None) -> str:
         """Queue a request.  ``prompt_embeds [P, H]`` (optional) replaces the token embeddings
         of the P prompt positions (reference: merge_prompt_embeds,
         vllm_neuron/functional/prompt_embeds.py:7); ``prompt_token_ids`` then only gives P."""
         params = SamplingParams.coerce(params)
         rid = request_id if request_id is not None else str(next(self._ids))
         req = Request(rid, list(prompt_token_ids), params, eos_token_id=self.eos_token_id,
-                      prompt_embeds=prompt_embeds)
+                      prompt_embeds=prompt_embeds, mm=mm)
         if params.structured_outputs:
             req.matcher = self.structured_outputs().matcher(params.structured_outputs)
             self._has_structured = True

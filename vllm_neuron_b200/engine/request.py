@@ -29,6 +29,7 @@ class Request:
     eos_token_id: int | None = None
     arrival_time: float = field(default_factory=time.perf_counter)
     prompt_embeds: object | None = None
+    mm: object | None = None    # MultiModalInputs (images of a vision-language model)
     output_token_ids: list[int] = field(default_factory=list)
     output_logprobs: list[float] = field(default_factory=list)
     status: RequestStatus = RequestStatus.WAITING

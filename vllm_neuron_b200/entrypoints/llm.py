@@ -51,7 +51,8 @@ class LLM:
                  skip_tokenizer_init: bool = False, num_gpu_blocks: int | None = None,
                  enforce_eager: bool = False, device: str | None = None, dtype: str = "auto",
                  async_scheduling: bool | None = None, speculative_config: dict | None = None,
-                 data_parallel_size: int | None = None, **unused):
+                 data_parallel_size: int | None = None, mm_processor_kwargs: dict | None = None,
+                 **unused):
         if device is None:
             device = f"cuda:{torch.cuda.current_device()}" if torch.cuda.is_available() else "cpu"
         ps.init_distributed(backend="gloo" if str(device).startswith("cpu") else None)
@@ -82,6 +83,7 @@ class LLM:
                           additional_config=additional_config or {},
                           speculative_config=speculative_config)
         self.engine = LLMEngine(args, tp=st.tp)
+        self.mm_processor_kwargs = mm_processor_kwargs
         self.tokenizer = None
         if not skip_tokenizer_init:
             path = tokenizer or (model if isinstance(model, str) else None)
@@ -125,6 +127,15 @@ class LLM:
                 emb = p["prompt_embeds"]
                 ids.append(self.engine.add_request([0] * emb.shape[0], sp, request_id=f"gen-{base}-{i}",
                                                    prompt_embeds=emb))
+                continue
+            if isinstance(p, dict) and p.get("multi_modal_data"):
+                from ..engine.multimodal import prepare_image_request
+
+                toks = _normalize_prompt(p, self.tokenizer)
+                images = p["multi_modal_data"].get("image")
+                toks, mm = prepare_image_request(toks, images, self.engine.model, self.engine.model_path,
+                                                 self.mm_processor_kwargs)
+                ids.append(self.engine.add_request(toks, sp, request_id=f"gen-{base}-{i}", mm=mm))
                 continue
             toks = _normalize_prompt(p, self.tokenizer)
             ids.append(self.engine.add_request(toks, sp, request_id=f"gen-{base}-{i}"))

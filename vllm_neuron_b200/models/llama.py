@@ -56,6 +56,9 @@ class ForwardBatch:
     want_hidden: bool = False  # return the final-norm hidden states of the logits rows (pooling)
     embed_rows: torch.Tensor | None = None   # [n] int64 batch rows whose embeddings are given
     embeds: torch.Tensor | None = None       # [n, H] the given embeddings (prompt_embeds)
+    positions3: torch.Tensor | None = None   # [T, 3] int32 M-RoPE positions (vision-language)
+    deep_rows: torch.Tensor | None = None    # [n] int64 rows receiving DeepStack features
+    deep_feats: torch.Tensor | None = None   # [n_deep, n, H] added after decoder layers 0..n_deep-1
 
 
 def _shard(n: int, world: int, rank: int) -> tuple[int, int]:
@@ -117,6 +120,7 @@ class LlamaForCausalLM(torch.nn.Module):
         self._alloc_workspace(max_tokens, max_decode_tokens, max_seqs)
         self.tp_fused = None  # TPFusedComm: fused all-reduce + residual + RMSNorm (decode)
         self.sequence_parallel = False  # prefill residual stream sharded over tokens (TP > 1)
+        self.mrope_section = None       # (t, h, w) frequency split of the multimodal RoPE
         self._sp = None                 # (padded tokens, local tokens) of the running SP forward
         self.sp_forwards = 0            # forwards that ran sequence-parallel
         # Hidden states captured after these layers (EAGLE3 drafting): [tokens, len * H]
@@ -231,13 +235,15 @@ class LlamaForCausalLM(torch.nn.Module):
                 ops.rope_kv_write(acc, b.positions, self.cos_sin, self.Hq, self.Hkv, self.D, q,
                                   k_cache, v_cache, b.slot_mapping, ly.q_norm, ly.k_norm, self.eps,
                                   rot_dim=self.cfg.rot_dim, clear_input=True, q_pos_scale=self.q_pos_scale,
-                                  qkv_bias=self._f32(ly, "qkv_bias"))
+                                  qkv_bias=self._f32(ly, "qkv_bias"), positions3=b.positions3,
+                                  mrope_section=self.mrope_section)
             else:
                 qkv = L.gemm_out(x[:T], ly.qkv, out=self.ws_qkv[:T])
                 ops.rope_kv_write(qkv, b.positions, self.cos_sin, self.Hq, self.Hkv, self.D, q,
                                   k_cache, v_cache, b.slot_mapping, ly.q_norm, ly.k_norm, self.eps,
                                   rot_dim=self.cfg.rot_dim, q_pos_scale=self.q_pos_scale,
-                                  qkv_bias=self._f32(ly, "qkv_bias"))
+                                  qkv_bias=self._f32(ly, "qkv_bias"), positions3=b.positions3,
+                                  mrope_section=self.mrope_section)
             attn = self.ws_attn[:T]
             self._attention(q, attn, k_cache, v_cache, b, window=ly.window, sinks=ly.sinks)
             nxt_norm = ly.post_norm
@@ -257,6 +263,11 @@ class LlamaForCausalLM(torch.nn.Module):
             # ---- MLP
             nxt_norm = self.layers[i + 1].input_norm if i + 1 < nL else self.final_norm
             self._mlp(i, ly, x, res, nxt_norm, Tg, small, fused)
+            if b.deep_feats is not None and i < b.deep_feats.shape[0]:
+                # DeepStack: visual features join the residual stream of the image-token rows
+                r = b.deep_rows
+                res.index_add_(0, r, b.deep_feats[i].to(res.dtype))
+                x.index_copy_(0, r, ops.rmsnorm(res.index_select(0, r), nxt_norm, self.eps).to(x.dtype))
             if self.aux_layers and i in self.aux_layers:
                 j = self.aux_layers.index(i)
                 self.aux_hidden[:T, j * self.H:(j + 1) * self.H].copy_(res)
@@ -289,7 +300,7 @@ class LlamaForCausalLM(torch.nn.Module):
         813-815,1096-1111; nn/embedding.py:236-241)."""
         tp = self.tp
         use_sp = (self.sequence_parallel and tp.world > 1 and not small and b.embed_rows is None
-                  and not self.aux_layers)
+                  and b.deep_feats is None and not self.aux_layers)
         if not use_sp:
             self._sp = None
             res = self.ws_residual[:T]

@@ -1,0 +1,251 @@
+"""Qwen3-VL (``Qwen3VLForConditionalGeneration``): a Qwen3 text decoder with interleaved
+multimodal RoPE and DeepStack visual features, plus a ViT image encoder.
+
+Vision encoder (``Qwen3VLVision``, replicated on every TP rank):
+
+    patches [N, C * Tp * P * P] -> linear patch embedding (+ bias)
+      + learned position table bilinearly interpolated to the image grid
+    depth x block: x += proj(attn(LN1(x)))   (full attention inside each image, 2-D rotary
+                                              embedding of the (row, column) patch position)
+                   x += fc2(gelu_tanh(fc1(LN2(x))))
+    merger: LN -> group 2 x 2 neighbouring patches -> fc1 -> GELU -> fc2  => text hidden size
+    DeepStack: after the blocks listed in ``deepstack_visual_indexes`` a merger of the same
+    form (LayerNorm after the grouping) produces features that are added to the text residual
+    stream at the image-token rows after decoder layers 0, 1, ...
+
+Text decoder: :class:`.llama.LlamaForCausalLM` with QK-norm; image-token rows take the merged
+vision embeddings (the prompt-embedding path of the runner) and rotate with 3-D positions
+(temporal, row, column) through the interleaved M-RoPE of the rope kernel; text tokens use
+(p, p, p), which equals the 1-D rotation, shifted by the request's position delta after an
+image.
+
+Reference: vllm_neuron/model/qwen3_vl/model_bf16.py, vision_encoder_bf16.py,
+utils/mrope.py (3-D positions), utils/merge_vision_embeds.py; the math follows the published
+Qwen3-VL definition (HF ``Qwen3VLForConditionalGeneration``).  The vision encoder runs its
+linear layers on the tcgen05 GEMM; its LayerNorm, GELU and per-image attention use torch ops.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+from ..ops import linear as L
+from .llama import LlamaForCausalLM
+
+
+def _lin(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None) -> torch.Tensor:
+    if x.is_cuda and x.dtype == torch.bfloat16 and x.shape[0] > 0:
+        y = L.gemm_out(x.contiguous(), w)
+    else:
+        y = (x.float() @ w.float().t()).to(x.dtype)
+    return y + b if b is not None else y
+
+
+class Qwen3VLVision(torch.nn.Module):
+    def __init__(self, vc: dict, device, dtype):
+        super().__init__()
+        self.hidden = vc["hidden_size"]
+        self.heads = vc["num_heads"]
+        self.depth = vc["depth"]
+        self.inter = vc["intermediate_size"]
+        self.patch = vc.get("patch_size", 16)
+        self.tpatch = vc.get("temporal_patch_size", 2)
+        self.in_ch = vc.get("in_channels", 3)
+        self.merge = vc.get("spatial_merge_size", 2)
+        self.out_hidden = vc["out_hidden_size"]
+        self.num_pos = vc.get("num_position_embeddings", 2304)
+        self.grid_side = int(round(math.sqrt(self.num_pos)))
+        self.deep_idx = list(vc.get("deepstack_visual_indexes") or [])
+        self.act = vc.get("hidden_act", "gelu_pytorch_tanh")
+        h, hm = self.hidden, self.hidden * self.merge ** 2
+        kw = dict(device=device, dtype=dtype)
+
+        def P(*shape):
+            return torch.nn.Parameter(torch.zeros(*shape, **kw), requires_grad=False)
+
+        self.patch_w = P(h, self.in_ch * self.tpatch * self.patch * self.patch)
+        self.patch_b = P(h)
+        self.pos_embed = P(self.num_pos, h)
+        self.blocks = torch.nn.ModuleList()
+        for _ in range(self.depth):
+            m = torch.nn.Module()
+            m.n1_w, m.n1_b, m.n2_w, m.n2_b = P(h), P(h), P(h), P(h)
+            m.qkv_w, m.qkv_b = P(3 * h, h), P(3 * h)
+            m.proj_w, m.proj_b = P(h, h), P(h)
+            m.fc1_w, m.fc1_b = P(self.inter, h), P(self.inter)
+            m.fc2_w, m.fc2_b = P(h, self.inter), P(h)
+            self.blocks.append(m)
+
+        def merger(post_norm: bool):
+            m = torch.nn.Module()
+            m.post_norm = post_norm
+            m.n_w, m.n_b = P(hm if post_norm else h), P(hm if post_norm else h)
+            m.fc1_w, m.fc1_b = P(hm, hm), P(hm)
+            m.fc2_w, m.fc2_b = P(self.out_hidden, hm), P(self.out_hidden)
+            return m
+
+        self.merger = merger(False)
+        self.deep_mergers = torch.nn.ModuleList([merger(True) for _ in self.deep_idx])
+        hd = h // self.heads
+        self.rot_inv_freq = 1.0 / (10000.0 ** (torch.arange(0, hd // 2, 2, dtype=torch.float32) / (hd // 2)))
+
+    # ---------------------------------------------------------------- position helpers
+    def _pos_embed(self, grids: list[tuple[int, int, int]]) -> torch.Tensor:
+        """Learned position table bilinearly resampled to each grid, in merge-block order."""
+        dev = self.pos_embed.device
+        out = []
+        n = self.grid_side
+        for t, h, w in grids:
+            hi = torch.linspace(0, n - 1, h)
+            wi = torch.linspace(0, n - 1, w)
+            h0, w0 = hi.int(), wi.int()
+            h1, w1 = (h0 + 1).clamp(max=n - 1), (w0 + 1).clamp(max=n - 1)
+            dh, dw = hi - h0, wi - w0
+            idx = [(h0[:, None] * n + w0[None]), (h0[:, None] * n + w1[None]),
+                   (h1[:, None] * n + w0[None]), (h1[:, None] * n + w1[None])]
+            wts = [(1 - dh)[:, None] * (1 - dw)[None], (1 - dh)[:, None] * dw[None],
+                   dh[:, None] * (1 - dw)[None], dh[:, None] * dw[None]]
+            pe = sum(self.pos_embed[i.flatten().to(dev)].float() * wt.flatten()[:, None].to(dev)
+                     for i, wt in zip(idx, wts)).to(self.pos_embed.dtype)
+            m = self.merge
+            pe = pe.repeat(t, 1).view(t, h // m, m, w // m, m, -1).permute(0, 1, 3, 2, 4, 5).reshape(t * h * w, -1)
+            out.append(pe)
+        return torch.cat(out)
+
+    def _rotary(self, grids) -> tuple[torch.Tensor, torch.Tensor]:
+        """cos / sin [N, head_dim] of the 2-D (row, column) rotary embedding, merge-block order."""
+        m = self.merge
+        rows, cols = [], []
+        for t, h, w in grids:
+            br = torch.arange(h // m)[:, None, None, None] * m + torch.arange(m)[None, None, :, None]
+            bc = torch.arange(w // m)[None, :, None, None] * m + torch.arange(m)[None, None, None, :]
+            r = br.expand(h // m, w // m, m, m).reshape(-1)
+            c = bc.expand(h // m, w // m, m, m).reshape(-1)
+            rows.append(r.repeat(t))
+            cols.append(c.repeat(t))
+        r, c = torch.cat(rows).float(), torch.cat(cols).float()
+        f = torch.cat([r[:, None] * self.rot_inv_freq[None], c[:, None] * self.rot_inv_freq[None]], 1)
+        emb = torch.cat([f, f], 1)
+        dev = self.pos_embed.device
+        return emb.cos().to(dev), emb.sin().to(dev)
+
+    # ---------------------------------------------------------------- forward
+    def _act(self, x: torch.Tensor) -> torch.Tensor:
+        return F.gelu(x, approximate="tanh") if "tanh" in self.act else F.gelu(x)
+
+    def _merge(self, m, x: torch.Tensor) -> torch.Tensor:
+        hm = self.hidden * self.merge ** 2
+        if m.post_norm:
+            x = F.layer_norm(x.view(-1, hm).float(), (hm,), m.n_w.float(), m.n_b.float(), 1e-6).to(x.dtype)
+        else:
+            x = F.layer_norm(x.float(), (self.hidden,), m.n_w.float(), m.n_b.float(), 1e-6).to(x.dtype).view(-1, hm)
+        x = F.gelu(_lin(x, m.fc1_w, m.fc1_b).float()).to(x.dtype)
+        return _lin(x, m.fc2_w, m.fc2_b)
+
+    @torch.no_grad()
+    def forward(self, pixels: torch.Tensor, grids: list[tuple[int, int, int]]):
+        """``pixels [N, C * Tp * P * P]`` -> (embeds ``[N / merge^2, out_hidden]``, DeepStack
+        features ``[len(deepstack), N / merge^2, out_hidden]``)."""
+        dt = self.patch_w.dtype
+        x = _lin(pixels.to(self.patch_w.device, dt), self.patch_w, self.patch_b)
+        x = x + self._pos_embed(grids)
+        cos, sin = self._rotary(grids)
+        lens = [t * h * w for t, h, w in grids]
+        H, nh = self.hidden, self.heads
+        hd = H // nh
+        deep = []
+        for li, blk in enumerate(self.blocks):
+            y = F.layer_norm(x.float(), (H,), blk.n1_w.float(), blk.n1_b.float(), 1e-6).to(dt)
+            qkv = _lin(y, blk.qkv_w, blk.qkv_b).view(-1, 3, nh, hd).float()
+            q, k, v = qkv[:, 0], qkv[:, 1], qkv[:, 2]
+            c, s = cos[:, None, :], sin[:, None, :]
+            q = q * c + torch.cat([-q[..., hd // 2:], q[..., :hd // 2]], -1) * s
+            k = k * c + torch.cat([-k[..., hd // 2:], k[..., :hd // 2]], -1) * s
+            q, k, v = q.to(dt), k.to(dt), v.to(dt)
+            outs = []
+            o0 = 0
+            for n in lens:  # full attention inside each image
+                qi, ki, vi = (z[o0:o0 + n].transpose(0, 1)[None] for z in (q, k, v))
+                outs.append(F.scaled_dot_product_attention(qi, ki, vi)[0].transpose(0, 1).reshape(n, H))
+                o0 += n
+            x = x + _lin(torch.cat(outs), blk.proj_w, blk.proj_b)
+            y = F.layer_norm(x.float(), (H,), blk.n2_w.float(), blk.n2_b.float(), 1e-6).to(dt)
+            y = self._act(_lin(y, blk.fc1_w, blk.fc1_b).float()).to(dt)
+            x = x + _lin(y, blk.fc2_w, blk.fc2_b)
+            if li in self.deep_idx:
+                deep.append(self._merge(self.deep_mergers[self.deep_idx.index(li)], x))
+        emb = self._merge(self.merger, x)
+        deep_t = torch.stack(deep) if deep else emb.new_zeros(0, emb.shape[0], emb.shape[1])
+        return emb, deep_t
+
+
+def mrope_positions(prompt: list[int], image_token_id: int, grids: list[tuple[int, int, int]],
+                    merge: int) -> tuple[np.ndarray, int]:
+    """3-D positions ``[3, P]`` of a prompt whose image placeholders are already expanded, and
+    the position delta of the tokens after the prompt (``pos = index + delta``).  Text tokens
+    count up by one; an image of grid (t, h, w) occupies (t h w) / merge^2 tokens at
+    (start, start + row, start + col) and advances the counter by max(h, w) / merge."""
+    P = len(prompt)
+    pos = np.zeros((3, P), dtype=np.int64)
+    cur = 0
+    i = 0
+    g = iter(grids)
+    while i < P:
+        if prompt[i] != image_token_id:
+            pos[:, i] = cur
+            cur += 1
+            i += 1
+            continue
+        t, h, w = next(g)
+        gh, gw = h // merge, w // merge
+        n = t * gh * gw
+        if prompt[i:i + n] != [image_token_id] * n:
+            raise ValueError("image placeholder count does not match the image grid")
+        pos[0, i:i + n] = cur
+        pos[1, i:i + n] = cur + np.repeat(np.arange(gh), gw * t)
+        pos[2, i:i + n] = cur + np.tile(np.arange(gw), gh * t)
+        cur += max(h, w) // merge
+        i += n
+    delta = int(pos.max()) + 1 - P if P else 0
+    return pos, delta
+
+
+class Qwen3VLForConditionalGeneration(LlamaForCausalLM):
+    supports_prefix_caching = False  # image tokens share ids: cached blocks would not match pixels
+
+    def __init__(self, cfg, *args, **kw):
+        super().__init__(cfg, *args, **kw)
+        raw = cfg.raw
+        vc = dict(raw.get("vision_config") or {})
+        vc.setdefault("out_hidden_size", self.H)
+        self.visual = Qwen3VLVision(vc, self.device, self.dtype)
+        rp = (raw.get("rope_parameters") or raw.get("rope_scaling") or {})
+        sec = rp.get("mrope_section") or [24, 20, 20]
+        self.mrope_section = (int(sec[0]), int(sec[1]), int(sec[2]))
+        self.image_token_id = int(raw.get("image_token_id", 151655))
+        self.spatial_merge = self.visual.merge
+
+    @torch.no_grad()
+    def init_random(self, seed: int = 0, std: float = 0.02):
+        super().init_random(seed, std)
+        g = torch.Generator(device=self.device)
+        g.manual_seed(seed * 1000 + 17)
+        for name, prm in self.visual.named_parameters():
+            if name.endswith("_w") and ("n1" in name or "n2" in name or name.startswith("n_") or ".n_" in name):
+                prm.fill_(1.0)
+            elif name.endswith("_b"):
+                prm.zero_()
+            else:
+                prm.normal_(0.0, std, generator=g)
+
+    def encode_images(self, pixels: torch.Tensor, grids: list[tuple[int, int, int]]):
+        return self.visual(pixels, grids)
+
+    def load_hf_state_dict(self, get_tensor, names: set[str]):
+        from ..utils.weight_loader import load_dense_decoder, load_qwen3_vl_vision
+
+        load_dense_decoder(self, get_tensor, names)
+        load_qwen3_vl_vision(self.visual, get_tensor, names)

@@ -16,6 +16,7 @@ _MODELS = {
     "GptOssForCausalLM": ("vllm_neuron_b200.models.gpt_oss", "GptOssForCausalLM"),
     "Qwen3MoeForCausalLM": ("vllm_neuron_b200.models.qwen_moe", "Qwen3MoeForCausalLM"),
     "Qwen2MoeForCausalLM": ("vllm_neuron_b200.models.qwen_moe", "Qwen2MoeForCausalLM"),
+    "Qwen3VLForConditionalGeneration": ("vllm_neuron_b200.models.qwen3_vl", "Qwen3VLForConditionalGeneration"),
     "Glm4MoeForCausalLM": ("vllm_neuron_b200.models.glm4_moe", "Glm4MoeForCausalLM"),
     "SyntheticForCausalLM": ("vllm_neuron_b200.models.synthetic", "SyntheticForCausalLM"),
     "Qwen3_5MoeForCausalLM": ("vllm_neuron_b200.models.qwen3_5", "Qwen3_5MoeForCausalLM"),

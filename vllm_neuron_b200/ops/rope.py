@@ -89,26 +89,29 @@ def rope_kv_write(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Ten
                   k_norm_w: torch.Tensor | None = None, eps: float = 1e-6,
                   rot_dim: int | None = None, neox: bool = True,
                   clear_input: bool = False, q_pos_scale: tuple[float, float] | None = None,
-                  qkv_bias: torch.Tensor | None = None) -> torch.Tensor:
+                  qkv_bias: torch.Tensor | None = None, positions3: torch.Tensor | None = None,
+                  mrope_section: tuple[int, int, int] | None = None) -> torch.Tensor:
     """Rotate q/k of ``qkv [T, (Hq + 2 Hkv) * D]``; write rotated q to ``q_out [T, Hq * D]`` and
     k/v into the paged cache at ``slot_mapping`` (int32, negative = skip).  ``q_pos_scale =
     (beta, period)`` multiplies the rotated q by ``1 + beta * log(1 + floor(pos / period))``
     (the long-context query temperature of Ministral-3 / Llama-4 configs).  ``qkv_bias`` (fp32
-    ``[(Hq + 2 Hkv) * D]``) is added to the input rows first."""
+    ``[(Hq + 2 Hkv) * D]``) is added to the input rows first.  ``positions3 [T, 3]`` with
+    ``mrope_section`` selects the interleaved multimodal RoPE of Qwen3-VL."""
     rot_dim = rot_dim or head_dim
     beta, period = q_pos_scale if q_pos_scale else (0.0, 1.0)
     if not qkv.is_cuda:
         src = qkv if qkv_bias is None else (qkv[:, :qkv_bias.numel()].float() + qkv_bias.float())
         rope_kv_write_ref(src, positions, cos_sin, num_q_heads, num_kv_heads, head_dim, q_out,
                           k_cache, v_cache, slot_mapping, q_norm_w, k_norm_w, eps, rot_dim, neox,
-                          q_pos_scale)
+                          q_pos_scale, positions3, mrope_section)
         if clear_input:
             qkv.zero_()
         return q_out
     ext().rope_kv_write(qkv, positions, slot_mapping, cos_sin, q_out, k_cache, v_cache,
                         q_norm_w, k_norm_w, eps, num_q_heads, num_kv_heads, head_dim, rot_dim,
                         neox, clear_input and qkv.dtype == torch.float32, float(beta), float(period),
-                        qkv_bias)
+                        qkv_bias, positions3, int(mrope_section[1]) if mrope_section else 0,
+                        int(mrope_section[2]) if mrope_section else 0)
     return q_out
 
 
@@ -126,8 +129,24 @@ def apply_rope_ref(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, neox: 
     return out
 
 
+def mrope_cos_sin(cos_sin: torch.Tensor, positions3: torch.Tensor, section) -> torch.Tensor:
+    """Per-token ``[T, rot_dim]`` cos|sin rows of the interleaved multimodal RoPE: frequency j
+    takes the height position when ``j % 3 == 1 and j < 3 * section[1]``, the width position
+    when ``j % 3 == 2 and j < 3 * section[2]``, the temporal position otherwise."""
+    half = cos_sin.shape[1] // 2
+    j = torch.arange(half)
+    comp = torch.zeros(half, dtype=torch.long)
+    comp[(j % 3 == 1) & (j < 3 * section[1])] = 1
+    comp[(j % 3 == 2) & (j < 3 * section[2])] = 2
+    pos = positions3.long()[:, comp]                      # [T, half]
+    cos = torch.gather(cos_sin[:, :half][pos.flatten()].view(-1, half, half), 2, j.view(1, -1, 1).expand(pos.shape[0], -1, 1))
+    sin = torch.gather(cos_sin[:, half:][pos.flatten()].view(-1, half, half), 2, j.view(1, -1, 1).expand(pos.shape[0], -1, 1))
+    return torch.cat([cos[..., 0], sin[..., 0]], 1)
+
+
 def rope_kv_write_ref(qkv, positions, cos_sin, Hq, Hkv, D, q_out, k_cache, v_cache,
-                      slot_mapping, q_norm_w, k_norm_w, eps, rot_dim, neox, q_pos_scale=None):
+                      slot_mapping, q_norm_w, k_norm_w, eps, rot_dim, neox, q_pos_scale=None,
+                      positions3=None, mrope_section=None):
     from .norm import rmsnorm_ref
 
     T = qkv.shape[0]
@@ -138,7 +157,7 @@ def rope_kv_write_ref(qkv, positions, cos_sin, Hq, Hkv, D, q_out, k_cache, v_cac
     if k_norm_w is not None:
         k = rmsnorm_ref(k, k_norm_w, eps).to(torch.bfloat16).float()
     half = rot_dim // 2
-    cs = cos_sin[positions.long()]
+    cs = mrope_cos_sin(cos_sin, positions3, mrope_section) if positions3 is not None else cos_sin[positions.long()]
     cos, sin = cs[:, :half], cs[:, half:rot_dim]
     q = torch.cat([apply_rope_ref(q[..., :rot_dim], cos, sin, neox), q[..., rot_dim:]], -1)
     k = torch.cat([apply_rope_ref(k[..., :rot_dim], cos, sin, neox), k[..., rot_dim:]], -1)

@@ -227,3 +227,29 @@ def load_qwen3_5(model, get_tensor: Callable[[str], torch.Tensor], names: set[st
     if cfg.tie_word_embeddings:
         return
     _copy(model.lm_head, shard_rows(get_tensor("lm_head.weight"), W, r, model.V_local), "lm_head")
+
+
+@torch.no_grad()
+def load_qwen3_vl_vision(vis, get_tensor: Callable[[str], torch.Tensor], names: set[str]):
+    """Qwen3-VL vision encoder (replicated on every rank): Conv3d patch embedding flattened to
+    a linear layer, position table, blocks, merger and DeepStack mergers."""
+    pre = "model.visual." if any(n.startswith("model.visual.") for n in names) else "visual."
+    w = get_tensor(pre + "patch_embed.proj.weight")
+    _copy(vis.patch_w, w.reshape(w.shape[0], -1), "patch_embed")
+    _copy(vis.patch_b, get_tensor(pre + "patch_embed.proj.bias"), "patch_embed.bias")
+    _copy(vis.pos_embed, get_tensor(pre + "pos_embed.weight"), "pos_embed")
+    for i, blk in enumerate(vis.blocks):
+        p = f"{pre}blocks.{i}."
+        for dst, src in ((blk.n1_w, "norm1.weight"), (blk.n1_b, "norm1.bias"), (blk.n2_w, "norm2.weight"),
+                         (blk.n2_b, "norm2.bias"), (blk.qkv_w, "attn.qkv.weight"), (blk.qkv_b, "attn.qkv.bias"),
+                         (blk.proj_w, "attn.proj.weight"), (blk.proj_b, "attn.proj.bias"),
+                         (blk.fc1_w, "mlp.linear_fc1.weight"), (blk.fc1_b, "mlp.linear_fc1.bias"),
+                         (blk.fc2_w, "mlp.linear_fc2.weight"), (blk.fc2_b, "mlp.linear_fc2.bias")):
+            _copy(dst, get_tensor(p + src), p + src)
+    mergers = [(vis.merger, pre + "merger.")] + [(m, f"{pre}deepstack_merger_list.{j}.")
+                                                   for j, m in enumerate(vis.deep_mergers)]
+    for m, p in mergers:
+        for dst, src in ((m.n_w, "norm.weight"), (m.n_b, "norm.bias"), (m.fc1_w, "linear_fc1.weight"),
+                         (m.fc1_b, "linear_fc1.bias"), (m.fc2_w, "linear_fc2.weight"),
+                         (m.fc2_b, "linear_fc2.bias")):
+            _copy(dst, get_tensor(p + src), p + src)

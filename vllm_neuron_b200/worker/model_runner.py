@@ -200,6 +200,10 @@ class ModelRunner:
                 ids[t:t + n] = (req.prompt_token_ids + req.output_token_ids)[st:st + n]
             p = np.arange(st, st + n, dtype=np.int32)
             pos[t:t + n] = p
+            mm = req.mm
+            if mm is not None:  # M-RoPE: temporal position in the prompt, index + delta after it
+                P_mm = mm.positions3.shape[1]
+                pos[t:t + n] = np.where(p < P_mm, mm.positions3[0, np.minimum(p, P_mm - 1)], p + mm.delta)
             blocks = np.asarray(req.block_ids, dtype=np.int32)
             slot[t:t + n] = blocks[p // bs] * bs + (p % bs)
             qst[i] = t
@@ -256,19 +260,64 @@ class ModelRunner:
         return s, w.decode, w.num_splits
 
     def _attach_prompt_embeds(self, out: SchedulerOutput, fb: ForwardBatch):
-        """Rows of this step that are prompt positions of requests with ``prompt_embeds``."""
+        """Rows of this step that are prompt positions of requests with ``prompt_embeds``, and
+        the image-token rows of vision-language requests (vision embeddings, DeepStack
+        features and 3-D M-RoPE positions; the vision encoder runs on a request's first
+        chunk and its output is kept until the prompt is prefilled)."""
         rows, parts = [], []
+        drows, dparts = [], []
+        need3 = False
         t = 0
         for sr in out.scheduled:
-            emb = sr.req.prompt_embeds
-            if emb is not None and sr.start < sr.req.num_prompt_tokens:
-                end = min(sr.start + sr.num_tokens, sr.req.num_prompt_tokens)
+            req = sr.req
+            emb = req.prompt_embeds
+            if emb is not None and sr.start < req.num_prompt_tokens:
+                end = min(sr.start + sr.num_tokens, req.num_prompt_tokens)
                 rows.extend(range(t, t + end - sr.start))
                 parts.append(emb[sr.start:end])
+            mm = req.mm
+            if mm is not None and sr.start < req.num_prompt_tokens:
+                end = min(sr.start + sr.num_tokens, req.num_prompt_tokens)
+                sel = mm.image_rows[(mm.image_rows >= sr.start) & (mm.image_rows < end)]
+                if len(sel):
+                    need3 = True
+                    if mm.emb is None:
+                        mm.emb, mm.deep = self.model.encode_images(mm.pixels.to(self.device), mm.grids)
+                    idx = torch.as_tensor([mm.row_of[int(r)] for r in sel], device=mm.emb.device)
+                    brows = [t + int(r) - sr.start for r in sel]
+                    rows.extend(brows)
+                    parts.append(mm.emb.index_select(0, idx))
+                    if mm.deep is not None and mm.deep.shape[0]:
+                        drows.extend(brows)
+                        dparts.append(mm.deep.index_select(1, idx))
+                if end >= req.num_prompt_tokens:  # prompt done: release the encoder cache
+                    mm.emb = mm.deep = None
             t += sr.num_tokens
+        pos3 = None
+        if need3:  # 3-D positions of every row of the step
+            pos3 = np.zeros((t, 3), dtype=np.int32)
+            t = 0
+            for sr in out.scheduled:
+                p = np.arange(sr.start, sr.start + sr.num_tokens)
+                mm = sr.req.mm
+                if mm is None:
+                    pos3[t:t + sr.num_tokens] = p[:, None]
+                else:
+                    P_mm = mm.positions3.shape[1]
+                    inside = p < P_mm
+                    pos3[t:t + sr.num_tokens] = np.where(inside[:, None], mm.positions3[:, np.minimum(p, P_mm - 1)].T,
+                                                         (p + mm.delta)[:, None])
+                t += sr.num_tokens
         if rows:
-            fb.embed_rows = torch.tensor(rows, dtype=torch.long).to(self.device, non_blocking=True)
-            fb.embeds = torch.cat(parts, 0).to(self.device, non_blocking=True)
+            order = np.argsort(rows, kind="stable")
+            fb.embed_rows = torch.tensor(np.asarray(rows)[order], dtype=torch.long).to(self.device, non_blocking=True)
+            cat = torch.cat([x.to(self.device) for x in parts], 0)
+            fb.embeds = cat.index_select(0, torch.as_tensor(order, device=cat.device))
+        if drows:
+            fb.deep_rows = torch.tensor(drows, dtype=torch.long).to(self.device, non_blocking=True)
+            fb.deep_feats = torch.cat(dparts, 1)
+        if pos3 is not None:
+            fb.positions3 = torch.from_numpy(np.ascontiguousarray(pos3)).to(self.device, non_blocking=True)
 
     def _snapshot(self, out: SchedulerOutput, lay: Layout, decode: bool, splits: int):
         """Save one step's device inputs (the packed int32 buffer and its layout)."""
@@ -446,6 +495,7 @@ class ModelRunner:
         dev.copy_(self.host_buf[:lay.total], non_blocking=self.is_cuda)
         fb, _ = self._views(dev, lay, B, S, W, decode, splits)
         fb.work = fb.work[:W]
+        self._attach_prompt_embeds(out, fb)
         fb.want_hidden = hidden
         logits = self.model.forward(fb).clone()
         if self.is_cuda:
