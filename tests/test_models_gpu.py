@@ -125,3 +125,40 @@ def test_ministral3_gpu_matches_cpu(cuda_device):
     d = tempfile.mkdtemp(prefix="ministral3_gpu_")
     hf.save_pretrained(d, safe_serialization=True)
     _agree(d)
+
+
+def test_qwen3_vl_gpu_matches_cpu(cuda_device):
+    """Image request on the GPU (bf16 kernels, vision linears on the tcgen05 GEMM) against the
+    fp32 CPU run of the same checkpoint: prompt logits close, same first tokens."""
+    import numpy as np
+    from transformers import Qwen3VLConfig, Qwen3VLForConditionalGeneration
+
+    IMG = 900
+    torch.manual_seed(0)
+    cfg = Qwen3VLConfig(
+        text_config=dict(hidden_size=256, num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
+                         head_dim=64, intermediate_size=512, vocab_size=1024, max_position_embeddings=1024,
+                         rope_parameters={"rope_type": "default", "rope_theta": 10000.0,
+                                          "mrope_section": [12, 10, 10], "mrope_interleaved": True},
+                         initializer_range=0.05, tie_word_embeddings=False),
+        vision_config=dict(hidden_size=64, intermediate_size=128, num_heads=2, depth=2, patch_size=8,
+                           temporal_patch_size=2, spatial_merge_size=2, out_hidden_size=256,
+                           num_position_embeddings=64, deepstack_visual_indexes=[0], initializer_range=0.05),
+        image_token_id=IMG, vision_start_token_id=901, vision_end_token_id=902, tie_word_embeddings=False)
+    hf = Qwen3VLForConditionalGeneration(cfg).to(torch.bfloat16).eval()
+    d = tempfile.mkdtemp(prefix="qwen3vl_gpu_")
+    hf.save_pretrained(d, safe_serialization=True)
+    img = (np.random.default_rng(0).random((48, 32, 3)) * 255).astype(np.uint8)
+    proc = {"min_pixels": 32 * 32, "max_pixels": 64 * 64}
+    prompt = {"prompt_token_ids": [5, 6, 901, IMG, 902, 7, 8, 9], "multi_modal_data": {"image": img}}
+    sp = SamplingParams(temperature=0, max_tokens=4, ignore_eos=True)
+    cpu = LLM(d, device="cpu", dtype="float32", max_num_seqs=2, max_model_len=256, num_gpu_blocks=64,
+              max_num_batched_tokens=256, mm_processor_kwargs=proc, skip_tokenizer_init=True)
+    ref = cpu.generate([prompt], sp)[0].outputs[0].token_ids
+    ext().reset_status()
+    gpu = LLM(d, device="cuda:0", max_num_seqs=2, max_model_len=256, num_gpu_blocks=64,
+              max_num_batched_tokens=256, mm_processor_kwargs=proc, skip_tokenizer_init=True)
+    got = gpu.generate([prompt], sp)[0].outputs[0].token_ids
+    torch.cuda.synchronize()
+    assert ext().read_status() == 0
+    assert got[:2] == ref[:2], (got, ref)
