@@ -360,7 +360,8 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
 
 // Raises a kernel's dynamic shared memory limit once per device.  Function attributes
 // belong to the device's context, so a process that drives several GPUs must set them on
-// each; `done` is a per-instantiation bitmask of the devices already configured.
+// each; `done` is a per-instantiation bitmask of the devices already configured.  Kernels
+// whose shared-memory size varies per call must pass the largest size any call may use.
 template <typename... KArgs>
 inline void set_max_dynamic_smem_once(void (*kernel)(KArgs...), int smem,
                                       std::atomic<uint64_t>& done) {

@@ -438,7 +438,8 @@ void moe_router_topk_launch(const __nv_bfloat16* x, long long ldx, const __nv_bf
   if (smem > 200 * 1024) throw std::invalid_argument("moe_router_topk: hidden size too large");
   if (T == 0) return;
   static std::atomic<uint64_t> configured{0};
-  set_max_dynamic_smem_once(moe_router_topk_kernel, smem, configured);
+  // the shared-memory size depends on H: opt in once to the largest size any call may use
+  set_max_dynamic_smem_once(moe_router_topk_kernel, 200 * 1024, configured);
   launch_pdl(moe_router_topk_kernel, dim3(T), dim3(256), smem, s, x, ldx, w, rows, H, bias, E, k,
              mode, renorm ? 1 : 0, scale, logits, ldl, ids, weights, shared_gate);
 }

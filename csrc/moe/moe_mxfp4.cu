@@ -260,7 +260,8 @@ void moe_mxfp4_gemm_launch(const __nv_bfloat16* x, long long ldx, const uint8_t*
   if (stages < 2) throw std::invalid_argument("moe_mxfp4_gemm: K too large for the X tile");
   const int smem = stages * kTileBytes + xbytes + bars;
   static std::atomic<uint64_t> configured{0};
-  set_max_dynamic_smem_once(moe_mxfp4_gemm_kernel, smem, configured);
+  // the shared-memory size depends on K: opt in once to the largest size any call may use
+  set_max_dynamic_smem_once(moe_mxfp4_gemm_kernel, 227 * 1024, configured);
   launch_pdl(moe_mxfp4_gemm_kernel, dim3(gmax, (N + kCols - 1) / kCols), dim3(32 * (kWarpsC + 1)), smem,
              s, x, ldx, wt, reinterpret_cast<const int4*>(gtiles), gcount, N, K, stages, y, ldy, status);
 }
