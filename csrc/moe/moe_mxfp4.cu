@@ -72,8 +72,9 @@ __device__ __forceinline__ bool consumers_sync_or(bool pred, int nthreads) {
 }
 
 constexpr int kRows = 16;    // token rows per pass (two n8 tensor-core tiles)
-constexpr int kWarpsC = 8;   // consumer warps, 32 weight columns (two m16 tiles) each
-constexpr int kCols = 32 * kWarpsC;
+constexpr int kMT = 2;        // m16 tiles (16 weight columns each) per consumer warp
+constexpr int kWarpsC = 8;   // consumer warps (16 warps x 1 tile measured no faster)
+constexpr int kCols = 16 * kMT * kWarpsC;
 constexpr int kPadK = 8;     // X row padding (halves) against ldmatrix bank conflicts
 constexpr int kTileW = kCols * 32;              // fp4 bytes of one (256 columns x 64 k) tile
 constexpr int kTileBytes = kTileW + kCols * 2;  // + 2 e8m0 scales per column
@@ -143,7 +144,7 @@ __global__ void __launch_bounds__(32 * (kWarpsC + 1), 1) moe_mxfp4_gemm_kernel(
   // ------------------------------------------------------------------------------ consumers
   constexpr int kThreadsC = 32 * kWarpsC;
   const int t = lane & 3, grp = lane >> 2;
-  const int n_base = blockIdx.y * kCols + warp * 32;
+  const int n_base = blockIdx.y * kCols + warp * 16 * kMT;
   int it = 0;
   bool bad = false;
   for (int pass = 0; pass < passes; ++pass) {
@@ -162,9 +163,9 @@ __global__ void __launch_bounds__(32 * (kWarpsC + 1), 1) moe_mxfp4_gemm_kernel(
     }
     consumers_sync_or(false, kThreadsC);
     const bool two = nr > 8;
-    float acc[2][2][4];
+    float acc[kMT][2][4];
 #pragma unroll
-    for (int m = 0; m < 2; ++m)
+    for (int m = 0; m < kMT; ++m)
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt) acc[m][nt][0] = acc[m][nt][1] = acc[m][nt][2] = acc[m][nt][3] = 0.f;
     for (int c = 0; c < KC; ++c, ++it) {
@@ -193,8 +194,8 @@ __global__ void __launch_bounds__(32 * (kWarpsC + 1), 1) moe_mxfp4_gemm_kernel(
       }
       const uint8_t* tile = ring + st * kTileBytes;
 #pragma unroll
-      for (int m = 0; m < 2; ++m) {
-        const int ra = warp * 32 + m * 16 + grp;  // weight column (A row) within the CTA's 256
+      for (int m = 0; m < kMT; ++m) {
+        const int ra = warp * 16 * kMT + m * 16 + grp;  // weight column (A row) within the CTA's 256
         const uint2 wl = *reinterpret_cast<const uint2*>(tile + ra * 32 + t * 8);
         const uint2 wh = *reinterpret_cast<const uint2*>(tile + (ra + 8) * 32 + t * 8);
         const uint32_t sl = *reinterpret_cast<const uint16_t*>(tile + kTileW + ra * 2);
@@ -230,7 +231,7 @@ __global__ void __launch_bounds__(32 * (kWarpsC + 1), 1) moe_mxfp4_gemm_kernel(
     if (bad) continue;
     // D fragment: (weight column grp [+8], token 2t [+1]) of each (m, n-tile).
 #pragma unroll
-    for (int m = 0; m < 2; ++m)
+    for (int m = 0; m < kMT; ++m)
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
