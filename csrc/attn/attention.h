@@ -31,6 +31,11 @@ struct PagedAttnParams {
   long long kv_rows;             // num_blocks * Hkv * block_size of one cache (0 = unknown)
   uint32_t* status;              // device status word for bounded waits (may be null)
   int* sched;                    // decode unit counters [2], zero between launches (may be null)
+  // FP8 KV cache: k_cache / v_cache hold e4m3 bytes in the same [blocks, Hkv, bs, D] layout;
+  // true values are byte * k_scale (folded into scale_log2 by the caller) and byte * v_scale
+  // (applied to the normalized output here).
+  int kv_fp8;
+  float v_scale;
 };
 
 void paged_attention_launch(const PagedAttnParams& p, int num_work, int head_dim, bool decode,

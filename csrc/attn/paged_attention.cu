@@ -18,6 +18,10 @@
 //                 K/V tile; the four partial softmax states are merged at the end.
 // K/V tiles are gathered from the block table with cp.async into XOR-swizzled shared
 // memory (double buffered) and multiplied on the tensor cores (bf16 mma, fp32 accum).
+// An FP8 (e4m3) cache keeps the same layout; its tiles are loaded into registers, widened to
+// bf16 (exact) and stored to the same tiles, with the per-tensor K scale folded into the
+// softmax scale and the V scale applied to the normalized output (the reference's FP8 KV
+// cache: vllm_neuron/utils/dtype_utils.py, functional/attention/attention_decode.py:527-651).
 // With more than one split, each split writes an fp32 partial output and its log-sum-exp
 // and attn_combine_kernel merges them.
 #include <cuda_bf16.h>
@@ -78,7 +82,16 @@ __device__ __forceinline__ uint32_t swz(int r, int c) {
 
 }  // namespace
 
-template <int D, bool DECODE>
+// Four e4m3 bytes -> four bf16 (two words), exact.
+__device__ __forceinline__ void e4m3x4_to_bf16x4(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t a = e4m3x2_to_f16x2(w), b = e4m3x2_to_f16x2(w >> 16);
+  const float2 fa = __half22float2(*reinterpret_cast<const __half2*>(&a));
+  const float2 fb = __half22float2(*reinterpret_cast<const __half2*>(&b));
+  lo = pack_bf16x2(fa.x, fa.y);
+  hi = pack_bf16x2(fb.x, fb.y);
+}
+
+template <int D, bool DECODE, bool FP8>
 __global__ void __launch_bounds__(128)
     paged_attention_kernel(const PagedAttnParams p) {
   pdl_trigger();
@@ -135,6 +148,40 @@ __global__ void __launch_bounds__(128)
 
   auto load_kv_tile = [&](int tile, int stage) {
     const int tok0 = tile * kKvTile;
+    if constexpr (FP8) {
+      // e4m3 cache: 16-byte loads widened to bf16 in registers and stored to the same
+      // swizzled bf16 tiles (the scales are applied to the scores and the output).
+      const uint8_t* k8 = reinterpret_cast<const uint8_t*>(p.k_cache);
+      const uint8_t* v8 = reinterpret_cast<const uint8_t*>(p.v_cache);
+      for (int i = threadIdx.x; i < kKvTile * (D / 16); i += blockDim.x) {
+        const int r = i / (D / 16), c = i % (D / 16);
+        const int tok = tok0 + r;
+        const bool valid = tok < kv_len;
+        const int page = valid ? tok / p.block_size : 0;
+        const int slot = tok - page * p.block_size;
+        const int blk = valid ? p.block_tables[(long long)b * p.bt_stride + page] : 0;
+        const long long off = (long long)blk * p.kv_block_stride +
+                              ((long long)kvh * p.block_size + slot) * D + c * 16;
+        uint4 kr = make_uint4(0u, 0u, 0u, 0u), vr = kr;
+        if (valid) {
+          kr = __ldg(reinterpret_cast<const uint4*>(k8 + off));
+          vr = __ldg(reinterpret_cast<const uint4*>(v8 + off));
+        }
+        uint4 k0, k1, v0, v1;
+        e4m3x4_to_bf16x4(kr.x, k0.x, k0.y);
+        e4m3x4_to_bf16x4(kr.y, k0.z, k0.w);
+        e4m3x4_to_bf16x4(kr.z, k1.x, k1.y);
+        e4m3x4_to_bf16x4(kr.w, k1.z, k1.w);
+        e4m3x4_to_bf16x4(vr.x, v0.x, v0.y);
+        e4m3x4_to_bf16x4(vr.y, v0.z, v0.w);
+        e4m3x4_to_bf16x4(vr.z, v1.x, v1.y);
+        e4m3x4_to_bf16x4(vr.w, v1.z, v1.w);
+        *reinterpret_cast<uint4*>(sK + stage * TILE_BYTES + swz<D>(r, 2 * c)) = k0;
+        *reinterpret_cast<uint4*>(sK + stage * TILE_BYTES + swz<D>(r, 2 * c + 1)) = k1;
+        *reinterpret_cast<uint4*>(sV + stage * TILE_BYTES + swz<D>(r, 2 * c)) = v0;
+        *reinterpret_cast<uint4*>(sV + stage * TILE_BYTES + swz<D>(r, 2 * c + 1)) = v1;
+      }
+    } else {
     for (int i = threadIdx.x; i < kKvTile * CH; i += blockDim.x) {
       const int r = i / CH, c = i % CH;
       const int tok = tok0 + r;
@@ -146,6 +193,7 @@ __global__ void __launch_bounds__(128)
                             ((long long)kvh * p.block_size + slot) * D + c * 8;
       cp_async16(sK + stage * TILE_BYTES + swz<D>(r, c), p.k_cache + off, valid);
       cp_async16(sV + stage * TILE_BYTES + swz<D>(r, c), p.v_cache + off, valid);
+    }
     }
   };
 
@@ -319,7 +367,7 @@ __global__ void __launch_bounds__(128)
       const int pr = row0 + r;
       const int tok = q_begin + pr / G;
       const int head = kvh * G + pr % G;
-      const float inv = ll > 0.f ? 1.f / ll : 0.f;
+      const float inv = (ll > 0.f ? 1.f / ll : 0.f) * (FP8 ? p.v_scale : 1.f);
       float acc[16];
       for (int c = 0; c < 16; ++c) {
         float v = 0.f;
@@ -350,7 +398,7 @@ __global__ void __launch_bounds__(128)
       const int pr = row0 + r;
       const int tok = q_begin + pr / G;
       const int head = kvh * G + pr % G;
-      const float inv = l_r[h] > 0.f ? 1.f / l_r[h] : 0.f;
+      const float inv = (l_r[h] > 0.f ? 1.f / l_r[h] : 0.f) * (FP8 ? p.v_scale : 1.f);
       if (p.num_splits == 1) {
         __nv_bfloat16* dst = p.out + (long long)tok * p.o_stride_t + (long long)head * D;
 #pragma unroll
@@ -405,17 +453,25 @@ __global__ void attn_combine_kernel(const float* __restrict__ part_o,
   }
 }
 
-template <int D, bool DECODE>
-static void launch_attn(const PagedAttnParams& p, int num_work, cudaStream_t stream) {
+template <int D, bool DECODE, bool FP8>
+static void launch_attn_t(const PagedAttnParams& p, int num_work, cudaStream_t stream) {
   constexpr int BM = DECODE ? 16 : 64;
   constexpr int smem = BM * D * 2 + 4 * kKvTile * D * 2;
   static_assert(!DECODE || (2 * 4 * 16 + 4 * 16 * D) * 4 <= 4 * kKvTile * D * 2,
                 "decode merge scratch must fit in the K/V tiles");
-  auto kern = paged_attention_kernel<D, DECODE>;
+  auto kern = paged_attention_kernel<D, DECODE, FP8>;
   static std::atomic<uint64_t> configured{0};
   set_max_dynamic_smem_once(kern, smem, configured);
   dim3 grid(num_work, p.Hkv, p.num_splits);
   launch_pdl(kern, grid, dim3(128), smem, stream, p);
+}
+
+template <int D, bool DECODE>
+static void launch_attn(const PagedAttnParams& p, int num_work, cudaStream_t stream) {
+  if (p.kv_fp8)
+    launch_attn_t<D, DECODE, true>(p, num_work, stream);
+  else
+    launch_attn_t<D, DECODE, false>(p, num_work, stream);
 }
 
 void paged_attention_launch(const PagedAttnParams& p, int num_work, int head_dim, bool decode,

@@ -18,6 +18,13 @@
 //     already in flight.  No CTA-wide barrier appears in the loop.
 //   * Math per tile: S = Q K^T (two m16n8k16 n-tiles), online softmax in the log2 domain,
 //     O += P V (D / 8 n-tiles), fp32 accumulation in registers.
+//   * FP8 (e4m3) cache: the same layout in bytes, so a tile is half the bytes and the ring has
+//     twice the stages.  ldmatrix reads the byte tiles as b16 matrices and cvt.e4m3x2 widens
+//     them to f16 fragments: for S the k order inside each 16-dim step is permuted (the Q
+//     fragments are loaded in the same order), for P V the transposed matrices give byte
+//     pairs of two neighbouring dims, split by byte permutes into an even-dim and an odd-dim
+//     n tile.  Q and P are f16; the K scale is folded into the softmax scale and the V scale
+//     into the output normalization.
 //
 // Chunks past the sequence end read the null block 0 (zeros), which keeps the byte count of
 // every stage constant.  Empty splits write a -inf log-sum-exp so the combine skips them.
@@ -68,6 +75,27 @@ __device__ __forceinline__ uint32_t kv_swz16(int r, int c) {
   return (uint32_t)((c >> 3) * (kTok * 128) + r * 128 + (((c & 7) ^ (r & 7)) << 4));
 }
 
+// FP8 tiles: one TMA box per BOXC bytes of the row (BOXC = min(D, 128)), 128-byte swizzle for
+// 128-byte rows, 64-byte swizzle for 64-byte rows (D = 64).
+template <int BOXC>
+__device__ __forceinline__ uint32_t kv_swz8(int r, int c) {
+  constexpr int CPB = BOXC / 16;  // 16-byte chunks per box row
+  const int box = c / CPB, cc = c % CPB;
+  if constexpr (BOXC == 128)
+    return (uint32_t)(box * (kTok * 128) + r * 128 + ((cc ^ (r & 7)) << 4));
+  else
+    return (uint32_t)(box * (kTok * 64) + r * 64 + ((cc ^ ((r >> 1) & 3)) << 4));
+}
+
+__device__ __forceinline__ void mma16816_f16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                             uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, "
+      "%7}, {%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
 struct Unit {
   int b, row0, kvh, split;
   int q_begin, kv_len, ctx0, rows_here, p_min, p_max;
@@ -104,13 +132,15 @@ __device__ __forceinline__ Unit unit_info(const PagedAttnParams& p, int u) {
 
 }  // namespace
 
-template <int D, int STAGES, int kWarps>
+template <int D, int STAGES, int kWarps, bool FP8>
 __global__ void __launch_bounds__(kWarps * 32, 1)
     paged_decode_kernel(const __grid_constant__ CUtensorMap tk,
                         const __grid_constant__ CUtensorMap tv, const PagedAttnParams p,
                         int num_units) {
-  constexpr int HALVES = D / 64;
-  constexpr int TILE_BYTES = kTok * D * 2;   // K or V of one tile
+  constexpr int BOXC = FP8 ? (D < 128 ? D : 128) : 64;  // columns per TMA box
+  constexpr int BOX_BYTES = kTok * (FP8 ? BOXC : 128);
+  constexpr int HALVES = D / BOXC;
+  constexpr int TILE_BYTES = kTok * D * (FP8 ? 1 : 2);  // K or V of one tile
   constexpr int STAGE_BYTES = 2 * TILE_BYTES;
   constexpr int QN = STAGES + 2;             // claimed units not yet finished
   constexpr unsigned FULL = 0xffffffffu;
@@ -163,8 +193,8 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
 #pragma unroll
     for (int h = 0; h < HALVES; ++h) {
-      tma_load_2d(&tk, &full[stage], dk + h * (kTok * 128), h * 64, y, policy);
-      tma_load_2d(&tv, &full[stage], dv + h * (kTok * 128), h * 64, y, policy);
+      tma_load_2d(&tk, &full[stage], dk + h * BOX_BYTES, h * BOXC, y, policy);
+      tma_load_2d(&tv, &full[stage], dv + h * BOX_BYTES, h * BOXC, y, policy);
     }
   };
 
@@ -238,13 +268,29 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     {
       const __nv_bfloat16* q0 = p.q + (long long)qrow_tok[0] * p.q_stride_t + (long long)qrow_head[0] * D;
       const __nv_bfloat16* q1 = p.q + (long long)qrow_tok[1] * p.q_stride_t + (long long)qrow_head[1] * D;
+      if constexpr (FP8) {
+        // f16 fragments in the k order of the fp8 K fragments: k slots (2t, 2t+1, 2t+8, 2t+9)
+        // of step k hold dims 16k + 4t + (0, 1, 2, 3).
 #pragma unroll
-      for (int k = 0; k < D / 16; ++k) {
-        const int c = k * 16 + t4 * 2;
-        qf[k][0] = rvalid[0] ? *reinterpret_cast<const uint32_t*>(q0 + c) : 0u;
-        qf[k][1] = rvalid[1] ? *reinterpret_cast<const uint32_t*>(q1 + c) : 0u;
-        qf[k][2] = rvalid[0] ? *reinterpret_cast<const uint32_t*>(q0 + c + 8) : 0u;
-        qf[k][3] = rvalid[1] ? *reinterpret_cast<const uint32_t*>(q1 + c + 8) : 0u;
+        for (int k = 0; k < D / 16; ++k) {
+          const int c = k * 16 + t4 * 4;
+          const uint2 z = make_uint2(0u, 0u);
+          const uint2 v0 = rvalid[0] ? *reinterpret_cast<const uint2*>(q0 + c) : z;
+          const uint2 v1 = rvalid[1] ? *reinterpret_cast<const uint2*>(q1 + c) : z;
+          qf[k][0] = bf16x2_to_f16x2_sat(v0.x);
+          qf[k][1] = bf16x2_to_f16x2_sat(v1.x);
+          qf[k][2] = bf16x2_to_f16x2_sat(v0.y);
+          qf[k][3] = bf16x2_to_f16x2_sat(v1.y);
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          const int c = k * 16 + t4 * 2;
+          qf[k][0] = rvalid[0] ? *reinterpret_cast<const uint32_t*>(q0 + c) : 0u;
+          qf[k][1] = rvalid[1] ? *reinterpret_cast<const uint32_t*>(q1 + c) : 0u;
+          qf[k][2] = rvalid[0] ? *reinterpret_cast<const uint32_t*>(q0 + c + 8) : 0u;
+          qf[k][3] = rvalid[1] ? *reinterpret_cast<const uint32_t*>(q1 + c + 8) : 0u;
+        }
       }
     }
     float o[D / 8][4];
@@ -268,15 +314,32 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
       float s[2][4];
 #pragma unroll
       for (int n = 0; n < 2; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+      if constexpr (FP8) {
+        // One 8x8 b16 matrix = 8 tokens x 16 fp8 dims; a lane's register holds dims
+        // 16c + 4t .. 4t + 3 of token g, i.e. the B fragment of one k step after widening.
 #pragma unroll
-      for (int k = 0; k < D / 16; ++k) {
-        const int i = lane >> 3;
-        const int r = (i >> 1) * 8 + (lane & 7);
-        const int c = k * 2 + (i & 1);
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4(smem_u32(k_s + kv_swz16(r, c)), b0, b1, b2, b3);
-        mma16816(s[0], qf[k], b0, b1);
-        mma16816(s[1], qf[k], b2, b3);
+        for (int k = 0; k < D / 16; k += 2) {
+          const int i = lane >> 3;
+          const int r = (i & 1) * 8 + (lane & 7);
+          const int c = k + (i >> 1);
+          uint32_t r0, r1, r2, r3;
+          ldsm_x4(smem_u32(k_s + kv_swz8<BOXC>(r, c)), r0, r1, r2, r3);
+          mma16816_f16(s[0], qf[k], e4m3x2_to_f16x2(r0), e4m3x2_to_f16x2(r0 >> 16));
+          mma16816_f16(s[1], qf[k], e4m3x2_to_f16x2(r1), e4m3x2_to_f16x2(r1 >> 16));
+          mma16816_f16(s[0], qf[k + 1], e4m3x2_to_f16x2(r2), e4m3x2_to_f16x2(r2 >> 16));
+          mma16816_f16(s[1], qf[k + 1], e4m3x2_to_f16x2(r3), e4m3x2_to_f16x2(r3 >> 16));
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          const int i = lane >> 3;
+          const int r = (i >> 1) * 8 + (lane & 7);
+          const int c = k * 2 + (i & 1);
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4(smem_u32(k_s + kv_swz16(r, c)), b0, b1, b2, b3);
+          mma16816(s[0], qf[k], b0, b1);
+          mma16816(s[1], qf[k], b2, b3);
+        }
       }
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
@@ -322,19 +385,45 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
         }
       }
       uint32_t a[4];
-      a[0] = pack_bf16x2(s[0][0], s[0][1]);
-      a[1] = pack_bf16x2(s[0][2], s[0][3]);
-      a[2] = pack_bf16x2(s[1][0], s[1][1]);
-      a[3] = pack_bf16x2(s[1][2], s[1][3]);
+      if constexpr (FP8) {
+        a[0] = pack_f16x2(s[0][0], s[0][1]);
+        a[1] = pack_f16x2(s[0][2], s[0][3]);
+        a[2] = pack_f16x2(s[1][0], s[1][1]);
+        a[3] = pack_f16x2(s[1][2], s[1][3]);
+        // Transposed 8x8 b16 matrices of the fp8 V tile: a lane's register holds bytes
+        // (token 2t, dim 2g), (2t, 2g + 1), (2t + 1, 2g), (2t + 1, 2g + 1) of a 16-dim chunk.
+        // Even and odd dims of chunk c are the n tiles 2c and 2c + 1.
 #pragma unroll
-      for (int n = 0; n < D / 8; n += 2) {
-        const int i = lane >> 3;
-        const int r = (i & 1) * 8 + (lane & 7);
-        const int c = n + (i >> 1);
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4_t(smem_u32(v_s + kv_swz16(r, c)), b0, b1, b2, b3);
-        mma16816(o[n], a, b0, b1);
-        mma16816(o[n + 1], a, b2, b3);
+        for (int c = 0; c < D / 16; c += 2) {
+          const int i = lane >> 3;
+          const int r = (i & 1) * 8 + (lane & 7);
+          const int cc = c + (i >> 1);
+          uint32_t r0, r1, r2, r3;
+          ldsm_x4_t(smem_u32(v_s + kv_swz8<BOXC>(r, cc)), r0, r1, r2, r3);
+          mma16816_f16(o[2 * c], a, e4m3x2_to_f16x2(__byte_perm(r0, 0u, 0x0020)),
+                       e4m3x2_to_f16x2(__byte_perm(r1, 0u, 0x0020)));
+          mma16816_f16(o[2 * c + 1], a, e4m3x2_to_f16x2(__byte_perm(r0, 0u, 0x0031)),
+                       e4m3x2_to_f16x2(__byte_perm(r1, 0u, 0x0031)));
+          mma16816_f16(o[2 * c + 2], a, e4m3x2_to_f16x2(__byte_perm(r2, 0u, 0x0020)),
+                       e4m3x2_to_f16x2(__byte_perm(r3, 0u, 0x0020)));
+          mma16816_f16(o[2 * c + 3], a, e4m3x2_to_f16x2(__byte_perm(r2, 0u, 0x0031)),
+                       e4m3x2_to_f16x2(__byte_perm(r3, 0u, 0x0031)));
+        }
+      } else {
+        a[0] = pack_bf16x2(s[0][0], s[0][1]);
+        a[1] = pack_bf16x2(s[0][2], s[0][3]);
+        a[2] = pack_bf16x2(s[1][0], s[1][1]);
+        a[3] = pack_bf16x2(s[1][2], s[1][3]);
+#pragma unroll
+        for (int n = 0; n < D / 8; n += 2) {
+          const int i = lane >> 3;
+          const int r = (i & 1) * 8 + (lane & 7);
+          const int c = n + (i >> 1);
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4_t(smem_u32(v_s + kv_swz16(r, c)), b0, b1, b2, b3);
+          mma16816(o[n], a, b0, b1);
+          mma16816(o[n + 1], a, b2, b3);
+        }
       }
       __syncwarp();  // every lane's reads of this stage are done before it is refilled
       ++cons_n;
@@ -347,7 +436,32 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     for (int h = 0; h < 2; ++h) {
       if (!rvalid[h]) continue;
       const int tok = qrow_tok[h], head = qrow_head[h];
-      const float inv = l_r[h] > 0.f ? 1.f / l_r[h] : 0.f;
+      const float inv = (l_r[h] > 0.f ? 1.f / l_r[h] : 0.f) * (FP8 ? p.v_scale : 1.f);
+      if constexpr (FP8) {
+        // n tiles 2c / 2c + 1 hold the even / odd dims of chunk c: dims 16c + 4t + (0..3)
+        // are o[2c][2h], o[2c + 1][2h], o[2c][2h + 1], o[2c + 1][2h + 1].
+        if (p.num_splits == 1) {
+          __nv_bfloat16* dst = p.out + (long long)tok * p.o_stride_t + (long long)head * D;
+#pragma unroll
+          for (int c = 0; c < D / 16; ++c)
+            *reinterpret_cast<uint2*>(dst + c * 16 + t4 * 4) =
+                make_uint2(pack_bf16x2(o[2 * c][h * 2] * inv, o[2 * c + 1][h * 2] * inv),
+                           pack_bf16x2(o[2 * c][h * 2 + 1] * inv, o[2 * c + 1][h * 2 + 1] * inv));
+        } else {
+          const long long rowi = ((long long)x.split * p.total_tokens + tok) * p.Hq + head;
+          float* dst = p.part_o + rowi * D;
+#pragma unroll
+          for (int c = 0; c < D / 16; ++c)
+            *reinterpret_cast<float4*>(dst + c * 16 + t4 * 4) =
+                make_float4(o[2 * c][h * 2] * inv, o[2 * c + 1][h * 2] * inv,
+                            o[2 * c][h * 2 + 1] * inv, o[2 * c + 1][h * 2 + 1] * inv);
+          if (t4 == 0) {
+            const float mu = m_r[h] == -INFINITY ? 0.f : m_r[h];
+            p.part_lse[rowi] = l_r[h] > 0.f ? mu + log2f(l_r[h]) : -INFINITY;
+          }
+        }
+        continue;
+      }
       if (p.num_splits == 1) {
         __nv_bfloat16* dst = p.out + (long long)tok * p.o_stride_t + (long long)head * D;
 #pragma unroll
@@ -388,12 +502,13 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
 namespace {
 // Per head dim: warps per CTA and ring stages per warp (16-token K+V stages of 64 * D bytes),
 // sized so the rings fill ~192 KB of shared memory with one CTA per SM.
-template <int D>
+// FP8 stages are half the bytes, so an FP8 ring has twice the stages in the same space.
+template <int D, bool FP8 = false>
 struct DecodeCfg {
   static constexpr int warps = D == 256 ? 4 : 8;
-  static constexpr int stages = D == 64 ? 6 : 3;
-  static constexpr int smem =
-      warps * stages * 2 * kTok * D * 2 + warps * stages * 8 + warps * (stages + 2) * 4 + 1024;
+  static constexpr int stages = (D == 64 ? 6 : 3) * (FP8 ? 2 : 1);
+  static constexpr int smem = warps * stages * 2 * kTok * D * (FP8 ? 1 : 2) + warps * stages * 8 +
+                              warps * (stages + 2) * 4 + 1024;
 };
 }  // namespace
 
@@ -401,12 +516,12 @@ int paged_decode_warps_per_cta(int head_dim) {
   return head_dim == 256 ? DecodeCfg<256>::warps : DecodeCfg<128>::warps;
 }
 
-template <int D>
+template <int D, bool FP8>
 static void launch_decode(const CUtensorMap& tk, const CUtensorMap& tv, const PagedAttnParams& p,
                           int num_units, cudaStream_t stream) {
-  using C = DecodeCfg<D>;
+  using C = DecodeCfg<D, FP8>;
   static_assert(C::smem <= 227 * 1024, "decode ring exceeds shared memory");
-  auto kern = paged_decode_kernel<D, C::stages, C::warps>;
+  auto kern = paged_decode_kernel<D, C::stages, C::warps, FP8>;
   static std::atomic<uint64_t> configured{0};
   set_max_dynamic_smem_once(kern, C::smem, configured);
   int grid = num_sms_cached();
@@ -426,17 +541,31 @@ bool paged_decode_tma_supported(const PagedAttnParams& p, int head_dim) {
 
 void paged_decode_tma_launch(const PagedAttnParams& p, int num_work, int head_dim,
                              cudaStream_t stream) {
+  const int num_units = num_work * p.Hkv * p.num_splits;
+  if (p.kv_fp8) {
+    const uint32_t boxc = head_dim < 128 ? (uint32_t)head_dim : 128u;
+    const CUtensorMap tk = make_tmap_u8_2d(p.k_cache, head_dim, (uint64_t)p.kv_rows, head_dim,
+                                           boxc, kTok, (int)boxc);
+    const CUtensorMap tv = make_tmap_u8_2d(p.v_cache, head_dim, (uint64_t)p.kv_rows, head_dim,
+                                           boxc, kTok, (int)boxc);
+    if (head_dim == 128)
+      launch_decode<128, true>(tk, tv, p, num_units, stream);
+    else if (head_dim == 256)
+      launch_decode<256, true>(tk, tv, p, num_units, stream);
+    else
+      launch_decode<64, true>(tk, tv, p, num_units, stream);
+    return;
+  }
   const CUtensorMap tk =
       make_tmap_bf16_2d(p.k_cache, head_dim, (uint64_t)p.kv_rows, head_dim, 64, kTok, true);
   const CUtensorMap tv =
       make_tmap_bf16_2d(p.v_cache, head_dim, (uint64_t)p.kv_rows, head_dim, 64, kTok, true);
-  const int num_units = num_work * p.Hkv * p.num_splits;
   if (head_dim == 128)
-    launch_decode<128>(tk, tv, p, num_units, stream);
+    launch_decode<128, false>(tk, tv, p, num_units, stream);
   else if (head_dim == 256)
-    launch_decode<256>(tk, tv, p, num_units, stream);
+    launch_decode<256, false>(tk, tv, p, num_units, stream);
   else
-    launch_decode<64>(tk, tv, p, num_units, stream);
+    launch_decode<64, false>(tk, tv, p, num_units, stream);
 }
 
 }  // namespace b200

@@ -113,10 +113,13 @@ void paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::T
                      const at::Tensor& q_start, const at::Tensor& work, at::Tensor& out,
                      c10::optional<at::Tensor> part_o, c10::optional<at::Tensor> part_lse,
                      c10::optional<at::Tensor> sinks, int64_t num_splits, int64_t num_kv_heads,
-                     int64_t window, double scale, bool decode) {
+                     int64_t window, double scale, bool decode, double k_scale, double v_scale) {
   CHECK_CUDA(q);
   CHECK_BF16(q);
-  CHECK_BF16(k_cache);
+  const bool fp8 = k_cache.scalar_type() == at::kFloat8_e4m3fn;
+  TORCH_CHECK(fp8 || k_cache.scalar_type() == at::kBFloat16,
+              "k_cache must be bfloat16 or float8_e4m3fn");
+  TORCH_CHECK(v_cache.scalar_type() == k_cache.scalar_type(), "k/v cache dtypes differ");
   TORCH_CHECK(q.dim() == 3, "q must be [T, Hq, D]");
   TORCH_CHECK(k_cache.dim() == 4, "k_cache must be [num_blocks, Hkv, block_size, D]");
   TORCH_CHECK(block_tables.scalar_type() == at::kInt && seq_lens.scalar_type() == at::kInt &&
@@ -153,7 +156,9 @@ void paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::T
   p.G = p.Hq / p.Hkv;
   p.block_size = (int)k_cache.size(2);
   p.window = (int)window;
-  p.scale_log2 = (float)(scale * 1.4426950408889634);
+  p.scale_log2 = (float)(scale * 1.4426950408889634 * (fp8 ? k_scale : 1.0));
+  p.kv_fp8 = fp8 ? 1 : 0;
+  p.v_scale = fp8 ? (float)v_scale : 1.f;
   p.total_tokens = (int)q.size(0);
   p.status = status_word();
   if (decode && k_cache.is_contiguous() && v_cache.is_contiguous()) {
@@ -193,7 +198,7 @@ void rope_kv_write(at::Tensor& qkv, const at::Tensor& positions,
                    int64_t num_kv_heads, int64_t head_dim, int64_t rot_dim, bool neox,
                    bool clear_input, double q_pos_beta, double q_pos_period,
                    c10::optional<at::Tensor> qkv_bias, c10::optional<at::Tensor> positions3,
-                   int64_t mrope_h, int64_t mrope_w) {
+                   int64_t mrope_h, int64_t mrope_w, double k_scale, double v_scale) {
   CHECK_CUDA(qkv);
   TORCH_CHECK(q_pos_beta == 0.0 || q_pos_period > 0.0, "rope_kv_write: q_pos_period must be positive");
   const c10::cuda::CUDAGuard guard(qkv.device());
@@ -211,6 +216,14 @@ void rope_kv_write(at::Tensor& qkv, const at::Tensor& positions,
     p.v_cache = reinterpret_cast<__nv_bfloat16*>(v_cache->data_ptr());
     p.kv_block_stride = k_cache->stride(0);
     p.block_size = (int)k_cache->size(2);
+    const bool fp8 = k_cache->scalar_type() == at::kFloat8_e4m3fn;
+    TORCH_CHECK(fp8 || k_cache->scalar_type() == at::kBFloat16,
+                "rope_kv_write: cache must be bfloat16 or float8_e4m3fn");
+    TORCH_CHECK(v_cache->scalar_type() == k_cache->scalar_type(), "k/v cache dtypes differ");
+    TORCH_CHECK(!fp8 || (k_scale > 0.0 && v_scale > 0.0), "fp8 KV scales must be positive");
+    p.kv_fp8 = fp8 ? 1 : 0;
+    p.k_inv_scale = fp8 ? (float)(1.0 / k_scale) : 1.f;
+    p.v_inv_scale = fp8 ? (float)(1.0 / v_scale) : 1.f;
   } else {
     p.slot_mapping = nullptr;
     p.block_size = 1;

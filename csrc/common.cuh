@@ -326,6 +326,23 @@ __device__ __forceinline__ float2 unpack_bf16x2(uint32_t v) {
   __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162*>(&v);
   return __bfloat1622float2(b);
 }
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+// Two e4m3 bytes (low byte -> low half) widened to f16x2 by the hardware converter; every
+// e4m3 value is exact in f16.
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t two_bytes) {
+  uint32_t d;
+  const unsigned short s = (unsigned short)(two_bytes & 0xffffu);
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(d) : "h"(s));
+  return d;
+}
+// bf16x2 -> f16x2 with the magnitude clamped to the f16 range.
+__device__ __forceinline__ uint32_t bf16x2_to_f16x2_sat(uint32_t v) {
+  const float2 f = unpack_bf16x2(v);
+  return pack_f16x2(fminf(fmaxf(f.x, -65504.f), 65504.f), fminf(fmaxf(f.y, -65504.f), 65504.f));
+}
 
 template <typename T>
 __device__ __forceinline__ T warp_sum(T v) {

@@ -37,6 +37,9 @@ struct GemmArgs {
 void gemm_bf16_launch(const GemmArgs& args, cudaStream_t stream);
 CUtensorMap make_tmap_bf16_2d(const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld,
                               uint32_t box_inner, uint32_t box_outer, bool swizzle128);
+// Byte-element 2-D map (fp8 data); swizzle_bytes is 0, 64 or 128.
+CUtensorMap make_tmap_u8_2d(const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld,
+                            uint32_t box_inner, uint32_t box_outer, int swizzle_bytes);
 int num_sms_cached();
 
 }  // namespace b200

@@ -474,6 +474,26 @@ CUtensorMap make_tmap_bf16_2d(const void* ptr, uint64_t inner, uint64_t outer, u
   return m;
 }
 
+CUtensorMap make_tmap_u8_2d(const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld,
+                            uint32_t box_inner, uint32_t box_outer, int swizzle_bytes) {
+  CUtensorMap m;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapSwizzle sw = swizzle_bytes == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                      : CU_TENSOR_MAP_SWIZZLE_NONE;
+  CUresult r = get_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr),
+                               dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    throw std::runtime_error("cuTensorMapEncodeTiled (u8) failed with code " +
+                             std::to_string((int)r));
+  return m;
+}
+
 template <int BN, int STAGES, int EPI>
 static void launch_impl(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
                         int grid, cudaStream_t stream) {

@@ -36,6 +36,10 @@ struct RopeKvParams {
   // q *= 1 + q_pos_beta * log(1 + floor(pos / q_pos_period)) after rotation (0: off)
   float q_pos_beta;
   float q_pos_period;
+  // FP8 (e4m3) cache: the caches hold bytes, written as satfinite(k * k_inv_scale) and
+  // satfinite(v * v_inv_scale).
+  int kv_fp8;
+  float k_inv_scale, v_inv_scale;
 };
 void rope_kv_write_launch(const RopeKvParams& p, void* qkv, bool qkv_is_f32, int T,
                           cudaStream_t stream);

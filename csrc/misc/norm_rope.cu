@@ -20,6 +20,8 @@
 #include <stdexcept>
 #include <string>
 
+#include <cuda_fp8.h>
+
 #include "../common.cuh"
 #include "misc.h"
 
@@ -287,11 +289,18 @@ __global__ void __launch_bounds__(256) rope_kv_write_kernel(const RopeKvParams p
     } else if (slot >= 0) {
       const int kvh = is_k ? h - p.Hq : h - p.Hq - p.Hkv;
       const long long blk = slot / p.block_size, off = slot % p.block_size;
-      __nv_bfloat16* cache = is_k ? p.k_cache : p.v_cache;
-      __nv_bfloat16* dst =
-          cache + blk * p.kv_block_stride + ((long long)kvh * p.block_size + off) * D;
+      const long long idx = blk * p.kv_block_stride + ((long long)kvh * p.block_size + off) * D;
+      if (p.kv_fp8) {
+        uint8_t* dst = reinterpret_cast<uint8_t*>(is_k ? p.k_cache : p.v_cache) + idx;
+        const float inv = is_k ? p.k_inv_scale : p.v_inv_scale;
 #pragma unroll
-      for (int e = 0; e < PER; ++e) dst[lane + 32 * e] = __float2bfloat16(v[e]);
+        for (int e = 0; e < PER; ++e)
+          dst[lane + 32 * e] = (uint8_t)__nv_cvt_float_to_fp8(v[e] * inv, __NV_SATFINITE, __NV_E4M3);
+      } else {
+        __nv_bfloat16* dst = (is_k ? p.k_cache : p.v_cache) + idx;
+#pragma unroll
+        for (int e = 0; e < PER; ++e) dst[lane + 32 * e] = __float2bfloat16(v[e]);
+      }
     }
     if (p.clear_input) {
 #pragma unroll

@@ -42,6 +42,7 @@ class EngineArgs:
     cuda_graphs: bool = True
     async_scheduling: bool | None = None  # default: on for CUDA devices
     additional_config: dict = field(default_factory=dict)
+    kv_cache_dtype: str = "auto"   # "auto" (model dtype) | "fp8" / "fp8_e4m3" (per-layer scales)
     # {"method": "ngram" | "eagle3", "num_speculative_tokens": k, "model": draft checkpoint,
     #  "prompt_lookup_min"/"prompt_lookup_max": n-gram sizes}
     speculative_config: dict | None = None
@@ -93,6 +94,10 @@ def build_model(args: EngineArgs, tp: GroupComm = SINGLE):
         model.init_random(seed=args.seed)
     else:
         load_checkpoint_into(model, model_path)
+    if args.kv_cache_dtype not in (None, "auto"):
+        if not hasattr(model, "set_kv_cache_dtype"):
+            raise ValueError(f"{type(model).__name__} does not support kv_cache_dtype={args.kv_cache_dtype!r}")
+        model.set_kv_cache_dtype(args.kv_cache_dtype, _kv_scales_from_checkpoint(model, model_path))
     real_group = tp.world > 1 and tp.group is not None
     if b200_config.sequence_parallel and hasattr(model, "sequence_parallel"):
         model.sequence_parallel = True
@@ -102,6 +107,32 @@ def build_model(args: EngineArgs, tp: GroupComm = SINGLE):
 
         model.enable_fused_comm(ps.get_parallel_state().cpu)
     return arch, model, model_path, device, b200_config
+
+
+def _kv_scales_from_checkpoint(model, model_path) -> list[tuple[float, float]] | None:
+    """Per-attention-layer ``self_attn.k_scale`` / ``self_attn.v_scale`` of an fp8-KV checkpoint
+    (true value = fp8 byte * scale); layers without them use 1.0 (reference:
+    vllm_neuron/model/llama3/model.py:2150-2180)."""
+    if model_path is None:
+        return None
+    from ..utils.checkpoints import SafetensorsCheckpoint
+
+    try:
+        ck = SafetensorsCheckpoint(model_path)
+    except (FileNotFoundError, OSError, ValueError):
+        return None
+    names = ck.names()
+    pre = "model.language_model." if any(n.startswith("model.language_model.") for n in names) else (
+        "model." if any(n.startswith("model.") for n in names) else "")
+    layers = getattr(model, "attn_layers", None) or list(range(model.num_kv_layers))
+    out = []
+    for l in layers:
+        pair = []
+        for nm in ("k_scale", "v_scale"):
+            key = f"{pre}layers.{l}.self_attn.{nm}"
+            pair.append(float(ck.get(key).float().reshape(-1)[0]) if key in names else 1.0)
+        out.append((pair[0], pair[1]))
+    return out
 
 
 def build_runner(args: EngineArgs, model, max_model_len: int, device, b200_config):

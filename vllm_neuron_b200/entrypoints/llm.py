@@ -52,7 +52,7 @@ class LLM:
                  enforce_eager: bool = False, device: str | None = None, dtype: str = "auto",
                  async_scheduling: bool | None = None, speculative_config: dict | None = None,
                  data_parallel_size: int | None = None, mm_processor_kwargs: dict | None = None,
-                 **unused):
+                 kv_cache_dtype: str = "auto", **unused):
         if device is None:
             device = f"cuda:{torch.cuda.current_device()}" if torch.cuda.is_available() else "cpu"
         ps.init_distributed(backend="gloo" if str(device).startswith("cpu") else None)
@@ -81,7 +81,7 @@ class LLM:
                           load_format=load_format, seed=seed, dtype=dtype, device=device,
                           cuda_graphs=not enforce_eager, async_scheduling=async_scheduling,
                           additional_config=additional_config or {},
-                          speculative_config=speculative_config)
+                          speculative_config=speculative_config, kv_cache_dtype=kv_cache_dtype)
         self.engine = LLMEngine(args, tp=st.tp)
         self.mm_processor_kwargs = mm_processor_kwargs
         self.tokenizer = None

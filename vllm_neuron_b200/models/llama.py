@@ -212,8 +212,35 @@ class LlamaForCausalLM(torch.nn.Module):
     def kv_cache_shape(self, num_blocks: int) -> tuple[int, ...]:
         return (num_blocks, self.Hkv, self.block_size, self.D)
 
+    @property
+    def kv_dtype(self) -> torch.dtype:
+        """Element type of the KV cache: the model dtype, or ``torch.float8_e4m3fn`` after
+        :meth:`set_kv_cache_dtype` ("fp8")."""
+        return getattr(self, "_kv_dtype", None) or self.dtype
+
+    def kv_scale(self, kv_layer: int) -> tuple[float, float]:
+        """Per-tensor (k_scale, v_scale) of an fp8 cache layer (1.0 when not quantized)."""
+        sc = getattr(self, "kv_scales", None)
+        return sc[kv_layer] if sc else (1.0, 1.0)
+
+    def set_kv_cache_dtype(self, kv_cache_dtype: str, scales: list[tuple[float, float]] | None = None):
+        """``"auto"`` keeps the model dtype; ``"fp8"`` / ``"fp8_e4m3"`` stores e4m3 K/V with
+        per-layer scales (true value = byte * scale; default 1.0), the reference's FP8 KV
+        cache (vllm_neuron/model/llama3/model.py:2150-2180)."""
+        if kv_cache_dtype in (None, "auto", "bfloat16", "bf16"):
+            self._kv_dtype = None
+            self.kv_scales = None
+            return
+        if kv_cache_dtype not in ("fp8", "fp8_e4m3"):
+            raise ValueError(f"unsupported kv_cache_dtype {kv_cache_dtype!r} (auto, fp8, fp8_e4m3)")
+        self._kv_dtype = torch.float8_e4m3fn
+        n = self.num_kv_layers
+        self.kv_scales = list(scales) if scales else [(1.0, 1.0)] * n
+        if len(self.kv_scales) != n:
+            raise ValueError(f"expected {n} KV scale pairs, got {len(self.kv_scales)}")
+
     def kv_bytes_per_block(self) -> int:
-        return 2 * self.num_kv_layers * self.Hkv * self.block_size * self.D * 2
+        return 2 * self.num_kv_layers * self.Hkv * self.block_size * self.D * self.kv_dtype.itemsize
 
     # ---------------------------------------------------------------- forward
     @torch.no_grad()
@@ -227,6 +254,7 @@ class LlamaForCausalLM(torch.nn.Module):
         nL = len(self.layers)
         for i, ly in enumerate(self.layers):
             k_cache, v_cache = self.kv_caches[i]
+            ks, vs = self.kv_scale(i)
             q = self.ws_q[:T]
             # ---- attention
             if small:
@@ -236,16 +264,17 @@ class LlamaForCausalLM(torch.nn.Module):
                                   k_cache, v_cache, b.slot_mapping, ly.q_norm, ly.k_norm, self.eps,
                                   rot_dim=self.cfg.rot_dim, clear_input=True, q_pos_scale=self.q_pos_scale,
                                   qkv_bias=self._f32(ly, "qkv_bias"), positions3=b.positions3,
-                                  mrope_section=self.mrope_section)
+                                  mrope_section=self.mrope_section, k_scale=ks, v_scale=vs)
             else:
                 qkv = L.gemm_out(x[:T], ly.qkv, out=self.ws_qkv[:T])
                 ops.rope_kv_write(qkv, b.positions, self.cos_sin, self.Hq, self.Hkv, self.D, q,
                                   k_cache, v_cache, b.slot_mapping, ly.q_norm, ly.k_norm, self.eps,
                                   rot_dim=self.cfg.rot_dim, q_pos_scale=self.q_pos_scale,
                                   qkv_bias=self._f32(ly, "qkv_bias"), positions3=b.positions3,
-                                  mrope_section=self.mrope_section)
+                                  mrope_section=self.mrope_section, k_scale=ks, v_scale=vs)
             attn = self.ws_attn[:T]
-            self._attention(q, attn, k_cache, v_cache, b, window=ly.window, sinks=ly.sinks)
+            self._attention(q, attn, k_cache, v_cache, b, window=ly.window, sinks=ly.sinks,
+                            kv_scale=(ks, vs))
             nxt_norm = ly.post_norm
             if small:
                 acc = self.acc_h[:T]
@@ -377,7 +406,8 @@ class LlamaForCausalLM(torch.nn.Module):
             self.tp.all_reduce_(acc)
             ops.add_rmsnorm(acc, res, norm_w, self.eps, out=x, clear_x=True)
 
-    def _attention(self, q, attn, k_cache, v_cache, b: ForwardBatch, window: int = 0, sinks=None):
+    def _attention(self, q, attn, k_cache, v_cache, b: ForwardBatch, window: int = 0, sinks=None,
+                   kv_scale: tuple[float, float] = (1.0, 1.0)):
         T = b.num_tokens
         ns = b.num_splits
         part_o = part_l = None
@@ -386,7 +416,8 @@ class LlamaForCausalLM(torch.nn.Module):
             part_l = self.ws_part_lse[: ns * T * self.Hq].view(ns, T, self.Hq)
         ops.paged_attention(q.view(T, self.Hq, self.D), k_cache, v_cache, b.block_tables, b.seq_lens,
                             b.q_start, b.work, b.decode, ns, self.scale, window=window, sinks=sinks,
-                            out=attn.view(T, self.Hq, self.D), part_o=part_o, part_lse=part_l)
+                            out=attn.view(T, self.Hq, self.D), part_o=part_o, part_lse=part_l,
+                            k_scale=kv_scale[0], v_scale=kv_scale[1])
 
     def compute_logits(self, x: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:
         S = idx.shape[0]

@@ -137,13 +137,14 @@ class Qwen3_5MoeForCausalLM(Qwen3MoeForCausalLM):
                 _linear(core, ly.out_proj, h)
             else:
                 k_cache, v_cache = self.kv_caches[self.kv_index[i]]
+                ks, vs = self.kv_scale(self.kv_index[i])
                 qkvg = _linear(x, ly.qkvg, self.ws_qkvg[:T])
                 q = self.ws_q[:T]
                 ops.rope_kv_write(qkvg[:, :self.qkv_out], b.positions, self.cos_sin, self.Hq, self.Hkv, self.D,
                                   q, k_cache, v_cache, b.slot_mapping, ly.q_norm, ly.k_norm, self.eps,
-                                  rot_dim=self.cfg.rot_dim)
+                                  rot_dim=self.cfg.rot_dim, k_scale=ks, v_scale=vs)
                 attn = self.ws_attn[:T]
-                self._attention(q, attn, k_cache, v_cache, b)
+                self._attention(q, attn, k_cache, v_cache, b, kv_scale=(ks, vs))
                 DN.sigmoid_gate_mul(attn, qkvg[:, self.qkv_out:])
                 _linear(attn, ly.o, h)
             tp.all_reduce_(h)

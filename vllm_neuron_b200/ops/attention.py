@@ -22,6 +22,7 @@ import torch
 
 from ._ext import ext
 
+FP8_MAX = 448.0   # largest finite float8_e4m3fn value
 PREFILL_ROWS = 64
 DECODE_ROWS = 16
 KV_TILE = 64
@@ -80,13 +81,18 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
                     work: torch.Tensor, decode: bool, num_splits: int, scale: float,
                     window: int = 0, sinks: torch.Tensor | None = None,
                     out: torch.Tensor | None = None, part_o: torch.Tensor | None = None,
-                    part_lse: torch.Tensor | None = None) -> torch.Tensor:
-    """Attention of ``q [T, Hq, D]`` over the paged cache; returns ``out [T, Hq, D]``."""
+                    part_lse: torch.Tensor | None = None, k_scale: float = 1.0,
+                    v_scale: float = 1.0) -> torch.Tensor:
+    """Attention of ``q [T, Hq, D]`` over the paged cache; returns ``out [T, Hq, D]``.
+
+    A ``torch.float8_e4m3fn`` cache holds ``K / k_scale`` and ``V / v_scale`` (per-tensor
+    scales, the reference's FP8 KV cache: vllm_neuron/utils/dtype_utils.py,
+    functional/attention/attention_decode.py:527-651); the kernels dequantize on load."""
     if out is None:
         out = torch.empty_like(q)
     if not q.is_cuda:
         out.copy_(paged_attention_ref(q, k_cache, v_cache, block_tables, seq_lens, q_start,
-                                      scale, window, sinks).to(out.dtype))
+                                      scale, window, sinks, k_scale, v_scale).to(out.dtype))
         return out
     T, Hq, D = q.shape
     if num_splits > 1 and (part_o is None or part_lse is None):
@@ -94,13 +100,16 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
         part_lse = torch.empty((num_splits, T, Hq), dtype=torch.float32, device=q.device)
     ext().paged_attention(q, k_cache, v_cache, block_tables, seq_lens, q_start, work, out,
                           part_o, part_lse, sinks, num_splits, k_cache.shape[1], window, scale,
-                          decode)
+                          decode, float(k_scale), float(v_scale))
     return out
 
 
 def paged_attention_ref(q, k_cache, v_cache, block_tables, seq_lens, q_start, scale,
-                        window=0, sinks=None) -> torch.Tensor:
-    """fp32 oracle: gathers each sequence's KV from its blocks and runs masked softmax."""
+                        window=0, sinks=None, k_scale=1.0, v_scale=1.0) -> torch.Tensor:
+    """fp32 oracle: gathers each sequence's KV from its blocks and runs masked softmax
+    (an fp8 cache is dequantized with its per-tensor scales)."""
+    fp8 = k_cache.dtype == torch.float8_e4m3fn
+    ks, vs = (float(k_scale), float(v_scale)) if fp8 else (1.0, 1.0)
     T, Hq, D = q.shape
     Hkv, bs = k_cache.shape[1], k_cache.shape[2]
     G = Hq // Hkv
@@ -114,8 +123,8 @@ def paged_attention_ref(q, k_cache, v_cache, block_tables, seq_lens, q_start, sc
             continue
         nblk = (L + bs - 1) // bs
         blocks = bt[b, :nblk].to(k_cache.device).long()
-        k = k_cache[blocks].float().permute(1, 0, 2, 3).reshape(Hkv, nblk * bs, D)[:, :L]
-        v = v_cache[blocks].float().permute(1, 0, 2, 3).reshape(Hkv, nblk * bs, D)[:, :L]
+        k = k_cache[blocks].float().permute(1, 0, 2, 3).reshape(Hkv, nblk * bs, D)[:, :L] * ks
+        v = v_cache[blocks].float().permute(1, 0, 2, 3).reshape(Hkv, nblk * bs, D)[:, :L] * vs
         k = k.repeat_interleave(G, dim=0)
         v = v.repeat_interleave(G, dim=0)
         qq = q[q0:q1].float().permute(1, 0, 2)  # [Hq, n, D]
@@ -135,3 +144,10 @@ def paged_attention_ref(q, k_cache, v_cache, block_tables, seq_lens, q_start, sc
             p = torch.softmax(s, dim=-1)
         out[q0:q1] = torch.einsum("hnl,hld->hnd", p, v).permute(1, 0, 2)
     return out
+
+
+def quantize_kv_fp8(x: torch.Tensor, scale: float) -> torch.Tensor:
+    """``x / scale`` saturated to the e4m3 range and rounded to ``torch.float8_e4m3fn`` (the
+    rule the KV-write kernel applies)."""
+    inv = torch.tensor(1.0 / float(scale), dtype=torch.float32)
+    return (x.float() * inv).clamp(-FP8_MAX, FP8_MAX).to(torch.float8_e4m3fn)

@@ -90,20 +90,23 @@ def rope_kv_write(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Ten
                   rot_dim: int | None = None, neox: bool = True,
                   clear_input: bool = False, q_pos_scale: tuple[float, float] | None = None,
                   qkv_bias: torch.Tensor | None = None, positions3: torch.Tensor | None = None,
-                  mrope_section: tuple[int, int, int] | None = None) -> torch.Tensor:
+                  mrope_section: tuple[int, int, int] | None = None, k_scale: float = 1.0,
+                  v_scale: float = 1.0) -> torch.Tensor:
     """Rotate q/k of ``qkv [T, (Hq + 2 Hkv) * D]``; write rotated q to ``q_out [T, Hq * D]`` and
     k/v into the paged cache at ``slot_mapping`` (int32, negative = skip).  ``q_pos_scale =
     (beta, period)`` multiplies the rotated q by ``1 + beta * log(1 + floor(pos / period))``
     (the long-context query temperature of Ministral-3 / Llama-4 configs).  ``qkv_bias`` (fp32
     ``[(Hq + 2 Hkv) * D]``) is added to the input rows first.  ``positions3 [T, 3]`` with
-    ``mrope_section`` selects the interleaved multimodal RoPE of Qwen3-VL."""
+    ``mrope_section`` selects the interleaved multimodal RoPE of Qwen3-VL.  A
+    ``torch.float8_e4m3fn`` cache receives ``k / k_scale`` and ``v / v_scale`` saturated to
+    the e4m3 range."""
     rot_dim = rot_dim or head_dim
     beta, period = q_pos_scale if q_pos_scale else (0.0, 1.0)
     if not qkv.is_cuda:
         src = qkv if qkv_bias is None else (qkv[:, :qkv_bias.numel()].float() + qkv_bias.float())
         rope_kv_write_ref(src, positions, cos_sin, num_q_heads, num_kv_heads, head_dim, q_out,
                           k_cache, v_cache, slot_mapping, q_norm_w, k_norm_w, eps, rot_dim, neox,
-                          q_pos_scale, positions3, mrope_section)
+                          q_pos_scale, positions3, mrope_section, k_scale, v_scale)
         if clear_input:
             qkv.zero_()
         return q_out
@@ -111,7 +114,8 @@ def rope_kv_write(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Ten
                         q_norm_w, k_norm_w, eps, num_q_heads, num_kv_heads, head_dim, rot_dim,
                         neox, clear_input and qkv.dtype == torch.float32, float(beta), float(period),
                         qkv_bias, positions3, int(mrope_section[1]) if mrope_section else 0,
-                        int(mrope_section[2]) if mrope_section else 0)
+                        int(mrope_section[2]) if mrope_section else 0, float(k_scale),
+                        float(v_scale))
     return q_out
 
 
@@ -146,7 +150,8 @@ def mrope_cos_sin(cos_sin: torch.Tensor, positions3: torch.Tensor, section) -> t
 
 def rope_kv_write_ref(qkv, positions, cos_sin, Hq, Hkv, D, q_out, k_cache, v_cache,
                       slot_mapping, q_norm_w, k_norm_w, eps, rot_dim, neox, q_pos_scale=None,
-                      positions3=None, mrope_section=None):
+                      positions3=None, mrope_section=None, k_scale=1.0, v_scale=1.0):
+    from .attention import quantize_kv_fp8
     from .norm import rmsnorm_ref
 
     T = qkv.shape[0]
@@ -172,6 +177,10 @@ def rope_kv_write_ref(qkv, positions, cos_sin, Hq, Hkv, D, q_out, k_cache, v_cac
             s = int(slot_mapping[t])
             if s < 0:
                 continue
-            k_cache[s // bs, :, s % bs] = k[t].to(k_cache.dtype)
-            v_cache[s // bs, :, s % bs] = v[t].to(v_cache.dtype)
+            if k_cache.dtype == torch.float8_e4m3fn:
+                k_cache[s // bs, :, s % bs] = quantize_kv_fp8(k[t], k_scale)
+                v_cache[s // bs, :, s % bs] = quantize_kv_fp8(v[t], v_scale)
+            else:
+                k_cache[s // bs, :, s % bs] = k[t].to(k_cache.dtype)
+                v_cache[s // bs, :, s % bs] = v[t].to(v_cache.dtype)
     return q_out

@@ -92,7 +92,8 @@ class B200Worker(WorkerBase):
             max_num_batched_tokens=sc.max_num_batched_tokens, max_model_len=mc.max_model_len,
             block_size=cc.block_size, load_format="dummy" if dummy else "auto", seed=mc.seed or 0,
             dtype=_DTYPES.get(mc.dtype, "bfloat16"), device=str(self.device),
-            additional_config=dict(self.vllm_config.additional_config or {}))
+            additional_config=dict(self.vllm_config.additional_config or {}),
+            kv_cache_dtype=str(getattr(cc, "cache_dtype", "auto") or "auto"))
 
     def load_model(self, *, load_dummy_weights: bool = False) -> None:
         args = self._engine_args(load_dummy_weights)
@@ -112,7 +113,7 @@ class B200Worker(WorkerBase):
     def get_kv_cache_spec(self) -> dict[str, KVCacheSpec]:
         m = self.model
         spec = FullAttentionSpec(block_size=self.cache_config.block_size, num_kv_heads=m.Hkv,
-                                 head_size=m.D, dtype=m.dtype)
+                                 head_size=m.D, dtype=getattr(m, "kv_dtype", m.dtype))
         return {f"layers.{i}.attn": spec for i in range(m.num_kv_layers)}
 
     def get_cache_block_size_bytes(self) -> int:

@@ -124,7 +124,7 @@ class ModelRunner:
         m = self.model
         n_kv = getattr(m, "num_kv_layers", m.cfg.num_layers)
         shape = (n_kv, 2) + m.kv_cache_shape(num_blocks)
-        self.kv_cache = torch.zeros(shape, dtype=m.dtype, device=self.device)
+        self.kv_cache = torch.zeros(shape, dtype=getattr(m, "kv_dtype", m.dtype), device=self.device)
         m.bind_kv_cache([(self.kv_cache[i, 0], self.kv_cache[i, 1]) for i in range(n_kv)])
         self.num_blocks = num_blocks
 
