@@ -187,13 +187,17 @@ def bench_moe(tp: int):
 def bench_deltanet(tp: int):
     """Gated DeltaNet layer of the Qwen3.6-A3B shape (16 key / 32 value heads x 128) per TP
     shard: prefill of 8 x 1024 tokens (one 8192-token chunk) and a 64-sequence decode step.
-    Time covers the q/k normalisation pass, the recurrence and the gated RMSNorm."""
+    Time covers the q/k normalisation pass, the recurrence (token by token, or the chunked WY
+    form for the prefill) and the gated RMSNorm."""
     from vllm_neuron_b200.ops import deltanet as DN
 
     Hk, Hv, d = 16 // tp, 32 // tp, 128
     dev = "cuda"
     rows = []
-    for name, q_lens, ctx in (("prefill_8x1024", [1024] * 8, [0] * 8), ("decode_b64", [1] * 64, [2048] * 64)):
+    for name, q_lens, ctx, mode in (("prefill_8x1024", [1024] * 8, [0] * 8, "recurrent"),
+                                    ("prefill_8x1024_chunked", [1024] * 8, [0] * 8, "chunked"),
+                                    ("prefill_2x4096_chunked", [4096] * 2, [0] * 2, "chunked"),
+                                    ("decode_b64", [1] * 64, [2048] * 64, "recurrent")):
         B = len(q_lens)
         qs = torch.tensor([0] + list(np.cumsum(q_lens)), dtype=torch.int32, device=dev)
         sl = torch.tensor([a + b for a, b in zip(q_lens, ctx)], dtype=torch.int32, device=dev)
@@ -208,8 +212,8 @@ def bench_deltanet(tp: int):
         state = torch.zeros(B, Hv, d, d, device=dev)
         out = torch.empty(T, Hv * d, device=dev, dtype=torch.bfloat16)
         ms = timeit(lambda: DN.gated_delta_rule(qkv, z, a, b, A_log, dt_bias, nw, 1e-6, qs, sl, slots,
-                                                state, out, Hk, Hv))
-        r = {"op": "gated_delta_rule", "case": name, "tp": tp, "T": T, "ms": ms,
+                                                state, out, Hk, Hv, mode=mode))
+        r = {"op": "gated_delta_rule", "case": name, "mode": mode, "tp": tp, "T": T, "ms": ms,
              "us_per_token_step": ms * 1e3 / max(q_lens)}
         print(json.dumps(r), flush=True)
         rows.append(r)

@@ -582,7 +582,7 @@ void gated_delta_rule(const at::Tensor& qkv, const at::Tensor& z, const at::Tens
                       const at::Tensor& b, const at::Tensor& A_log, const at::Tensor& dt_bias,
                       const at::Tensor& norm_w, double eps, const at::Tensor& q_start,
                       const at::Tensor& seq_lens, const at::Tensor& slots, at::Tensor& state,
-                      at::Tensor& out, int64_t Hk, int64_t Hv) {
+                      at::Tensor& out, int64_t Hk, int64_t Hv, int64_t mode) {
   CHECK_CUDA(qkv);
   CHECK_BF16(qkv);
   CHECK_BF16(z);
@@ -613,9 +613,28 @@ void gated_delta_rule(const at::Tensor& qkv, const at::Tensor& z, const at::Tens
   p.T = (int)out.size(0);
   at::Tensor gb = at::empty({std::max<int64_t>(p.T, 1), Hv, 4}, qkv.options().dtype(at::kFloat));
   p.gb = reinterpret_cast<float4*>(gb.data_ptr<float>());
+  const int64_t B = seq_lens.size(0);
+  // mode 0: chunked for prefill-sized steps (at least 128 tokens, 2 per sequence on average),
+  // recurrent otherwise; 1: recurrent; 2: chunked
+  const bool chunked = mode == 2 || (mode == 0 && p.T >= 128 && p.T >= 2 * B);
+  if (chunked && B > 0 && p.T > 0) {
+    const int64_t max_chunks = p.T / 64 + B;
+    const auto f32 = qkv.options().dtype(at::kFloat);
+    at::Tensor W = at::empty({p.T, Hv, 128}, f32), U = at::empty({p.T, Hv, 128}, f32);
+    at::Tensor QKm = at::empty({max_chunks, Hv, 64, 64}, f32), lg = at::empty({p.T, Hv}, f32);
+    at::Tensor chunks = at::empty({max_chunks, 4}, qkv.options().dtype(at::kInt));
+    at::Tensor seq0 = at::empty({B + 1}, qkv.options().dtype(at::kInt));
+    b200::GdnChunkScratch cs{W.data_ptr<float>(), U.data_ptr<float>(), QKm.data_ptr<float>(),
+                             lg.data_ptr<float>(), reinterpret_cast<int4*>(chunks.data_ptr<int>()),
+                             seq0.data_ptr<int>(), (int)max_chunks};
+    b200::gated_delta_rule_chunked_launch(p, linear_batch(q_start, seq_lens, slots), cs, cur_stream());
+    // norms / gates, chunk table, per-chunk solve, state pass, gated RMSNorm
+    check_launch("gated_delta_rule", 5);
+    return;
+  }
   b200::gated_delta_rule_launch(p, linear_batch(q_start, seq_lens, slots), cur_stream());
   // normalisation / gates pass, recurrence, gated RMSNorm
-  check_launch("gated_delta_rule", seq_lens.size(0) > 0 ? (p.T > 0 ? 3 : 1) : 0);
+  check_launch("gated_delta_rule", B > 0 ? (p.T > 0 ? 3 : 1) : 0);
 }
 
 void sigmoid_gate_mul(at::Tensor& x, const at::Tensor& gate) {

@@ -19,8 +19,12 @@
 //                      reduces over dk with shuffles, so tokens are processed in order (the
 //                      recurrence) without CTA barriers, next-token inputs prefetched; the
 //                      gated RMSNorm over dv runs afterwards (one warp per token and head).
+//   chunked form       prefill-sized steps: the WY form over 64-token chunks (below), with
+//                      the intra-chunk products on the tensor cores and the state carried in
+//                      fp32 across the chunks of a sequence.
 #include <cuda_bf16.h>
 
+#include <atomic>
 #include <stdexcept>
 
 #include "../common.cuh"
@@ -261,6 +265,387 @@ __global__ void sigmoid_gate_mul_kernel(__nv_bfloat16* __restrict__ x, long long
   }
 }
 
+
+// ------------------------------------------------------------------------------------------
+// Chunked (WY) gated delta rule.  Within a chunk of L <= 64 tokens with entering state S0,
+// lg_t = sum_{s<=t} log g_s (from the chunk start), gamma_t = exp(lg_t), unit-norm k^ and
+// q^ (q^ also scaled by dk^-1/2), the per-token writes delta_t of the recurrence satisfy
+//
+//   (I + A) Delta = diag(beta) V - diag(beta gamma) K^ S0,  A[t,s] = beta_t e^{lg_t-lg_s} k^_t.k^_s (s<t)
+//
+// so Delta = U - W S0 with W = (I + A)^-1 diag(beta gamma) K^ and U = (I + A)^-1 diag(beta) V.
+// Then  o_t = gamma_t S0^T q^_t + sum_{s<=t} e^{lg_t-lg_s} (q^_t.k^_s) delta_s   and
+//       S_L = gamma_L S0 + sum_s e^{lg_L-lg_s} k^_s delta_s^T.
+// gdn_chunk_prep_kernel computes W, U and the masked Q^K^T of every (chunk, value head) in
+// parallel (K^K^T and Q^K^T on the tensor cores, the unit lower-triangular solve by forward
+// substitution, one thread per right-hand-side column); gdn_chunk_state_kernel walks the chunks
+// of one sequence in order for 32 value columns of one head, in fp32.
+// ------------------------------------------------------------------------------------------
+namespace {
+constexpr int kGC = 64;  // chunk length
+
+__device__ __forceinline__ void gdn_ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1,
+                                            uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void gdn_mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                        uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, "
+      "%7}, {%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// [64 rows][128] bf16 tile, 16-byte chunks XOR-swizzled by row (conflict-free ldmatrix)
+__device__ __forceinline__ uint32_t gdn_swz(int r, int c) {
+  return (uint32_t)(r * 256 + ((c ^ (r & 7)) << 4));
+}
+}  // namespace
+
+__global__ void gdn_chunk_table_kernel(LinearAttnBatch bt, int4* chunks, int* seq_chunk0) {
+  pdl_trigger();
+  pdl_wait();
+  if (threadIdx.x != 0) return;
+  int c = 0;
+  for (int b = 0; b < bt.B; ++b) {
+    seq_chunk0[b] = c;
+    const int t0 = bt.q_start[b], n = bt.q_start[b + 1] - t0;
+    for (int s = 0; s < n; s += kGC) chunks[c++] = make_int4(t0 + s, min(kGC, n - s), b, 0);
+  }
+  seq_chunk0[bt.B] = c;
+}
+
+// grid (max_chunks, Hv), 256 threads; dynamic smem = kGdnPrepSmem
+constexpr int kGdnPrepSmem = 2 * kGC * 128 * 2 + 2 * kGC * 65 * 4 + 2 * kGC * 4;
+
+__global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(const GatedDeltaParams p,
+                                                             GdnChunkScratch cs, int B) {
+  pdl_trigger();
+  pdl_wait();
+  const int c = blockIdx.x, h = blockIdx.y;
+  if (c >= cs.seq_chunk0[B]) return;
+  const int4 ch = cs.chunks[c];
+  const int t0 = ch.x, L = ch.y;
+  const int kh = h / (p.Hv / p.Hk);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  extern __shared__ __align__(128) uint8_t gsm[];
+  uint8_t* sq = gsm;                                   // q^ [64][128] bf16
+  uint8_t* sk = sq + kGC * 256;                        // k^ [64][128] bf16
+  float* sKK = reinterpret_cast<float*>(sk + kGC * 256);  // [64][65]: K^K^T, then A
+  float* sQK = sKK + kGC * 65;                          // [64][65]: Q^K^T
+  float* slg = sQK + kGC * 65;                          // [64]
+  float* sbeta = slg + kGC;                             // [64]
+
+  if (tid < kGC) {
+    float lg = 0.f, beta = 0.f;
+    if (tid < L) {
+      const long long t = t0 + tid;
+      const float a = __bfloat162float(p.a[t * p.ld_zab + h]);
+      lg = -__expf(p.A_log[h]) * softplus_d(a + p.dt_bias[h]);
+      beta = p.gb[t * p.Hv + h].y;
+    }
+    slg[tid] = lg;
+    sbeta[tid] = beta;
+  }
+  // q^ = q / |q| * dk^-1/2 and k^ = k / |k|, rounded to bf16 for the tensor cores
+  const float qscale = rsqrtf(128.f);
+  for (int i = tid; i < kGC * 16; i += 256) {
+    const int r = i >> 4, cc = i & 15;
+    uint4 qo = make_uint4(0u, 0u, 0u, 0u), ko = qo;
+    if (r < L) {
+      const long long t = t0 + r;
+      const float4 gb = p.gb[t * p.Hv + h];
+      const __nv_bfloat16* row = p.qkv + t * p.ld_qkv;
+      const uint4 qi = *reinterpret_cast<const uint4*>(row + (long long)kh * 128 + cc * 8);
+      const uint4 ki = *reinterpret_cast<const uint4*>(row + (long long)(p.Hk + kh) * 128 + cc * 8);
+      const uint32_t qw[4] = {qi.x, qi.y, qi.z, qi.w}, kw[4] = {ki.x, ki.y, ki.z, ki.w};
+      uint32_t qn[4], kn[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 fq = unpack_bf16x2(qw[e]), fk = unpack_bf16x2(kw[e]);
+        const float sq_ = gb.z * qscale;
+        qn[e] = pack_bf16x2(fq.x * sq_, fq.y * sq_);
+        kn[e] = pack_bf16x2(fk.x * gb.w, fk.y * gb.w);
+      }
+      qo = make_uint4(qn[0], qn[1], qn[2], qn[3]);
+      ko = make_uint4(kn[0], kn[1], kn[2], kn[3]);
+    }
+    *reinterpret_cast<uint4*>(sq + gdn_swz(r, cc)) = qo;
+    *reinterpret_cast<uint4*>(sk + gdn_swz(r, cc)) = ko;
+  }
+  __syncthreads();
+  if (tid == 0) {  // inclusive prefix sum of the log decays
+    float acc = 0.f;
+    for (int t = 0; t < kGC; ++t) {
+      acc += slg[t];
+      slg[t] = acc;
+    }
+  }
+  // K^K^T (warps 0-3) and Q^K^T (warps 4-7): 16 rows x 64 columns per warp, k = 128
+  {
+    const uint8_t* sa = warp < 4 ? sk : sq;
+    float* dst = warp < 4 ? sKK : sQK;
+    const int wrow = (warp & 3) * 16;
+    float acc[8][4];
+#pragma unroll
+    for (int n = 0; n < 8; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      uint32_t af[4];
+      gdn_ldsm_x4(smem_u32(sa + gdn_swz(wrow + (lane & 15), k * 2 + (lane >> 4))), af[0], af[1],
+                  af[2], af[3]);
+#pragma unroll
+      for (int n = 0; n < 8; n += 2) {
+        const int i = lane >> 3;
+        const int r = n * 8 + (i >> 1) * 8 + (lane & 7);
+        uint32_t b0, b1, b2, b3;
+        gdn_ldsm_x4(smem_u32(sk + gdn_swz(r, k * 2 + (i & 1))), b0, b1, b2, b3);
+        gdn_mma(acc[n], af, b0, b1);
+        gdn_mma(acc[n + 1], af, b2, b3);
+      }
+    }
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      const int r = wrow + (lane >> 2), col = n * 8 + (lane & 3) * 2;
+      dst[r * 65 + col] = acc[n][0];
+      dst[r * 65 + col + 1] = acc[n][1];
+      dst[(r + 8) * 65 + col] = acc[n][2];
+      dst[(r + 8) * 65 + col + 1] = acc[n][3];
+    }
+  }
+  __syncthreads();
+  // A (strictly lower, in place of K^K^T) and the decay-masked Q^K^T (written out)
+  float* qkm = cs.QKm + ((long long)c * p.Hv + h) * (kGC * kGC);
+  for (int i = tid; i < kGC * kGC; i += 256) {
+    const int t = i >> 6, s2 = i & 63;
+    float a = 0.f, q = 0.f;
+    if (t < L && s2 <= t) {
+      const float dec = __expf(slg[t] - slg[s2]);
+      q = dec * sQK[t * 65 + s2];
+      if (s2 < t) a = sbeta[t] * dec * sKK[t * 65 + s2];
+    }
+    sKK[t * 65 + s2] = a;
+    qkm[i] = q;
+  }
+  __syncthreads();
+  // Forward substitution (I + A) X = R, one right-hand-side column per thread:
+  // columns 0..127 -> W (R = beta gamma k^), 128..255 -> U (R = beta v).
+  const int j = tid;
+  const bool isw = j < 128;
+  const __nv_bfloat16* vcol = p.qkv + (long long)t0 * p.ld_qkv + 2LL * p.Hk * 128 +
+                              (long long)h * 128 + (j & 127);
+  float x[kGC];
+#pragma unroll
+  for (int t = 0; t < kGC; ++t) {
+    float r = 0.f;
+    if (t < L) {
+      if (isw) {
+        const __nv_bfloat16* kp = reinterpret_cast<const __nv_bfloat16*>(
+            sk + gdn_swz(t, j >> 3) + (j & 7) * 2);
+        r = sbeta[t] * __expf(slg[t]) * __bfloat162float(*kp);
+      } else {
+        r = sbeta[t] * __bfloat162float(vcol[(long long)t * p.ld_qkv]);
+      }
+    }
+#pragma unroll
+    for (int s2 = 0; s2 < t; ++s2) r = fmaf(-sKK[t * 65 + s2], x[s2], r);
+    x[t] = r;
+  }
+  float* dst = (isw ? cs.W : cs.U) + ((long long)t0 * p.Hv + h) * 128 + (j & 127);
+#pragma unroll
+  for (int t = 0; t < kGC; ++t)
+    if (t < L) dst[(long long)t * p.Hv * 128] = x[t];
+  if (tid < L) cs.lg[(long long)(t0 + tid) * p.Hv + h] = slg[tid];
+}
+
+// grid (B, Hv, 4), 256 threads: 32 value columns of one (sequence, value head), all chunks
+// of the sequence in order.  Thread (ty = tid / 8, tx = tid % 8) owns value columns 4tx..4tx+3
+// and rows 2ty, 2ty+1 of the chunk outputs, or rows 4ty..4ty+3 of the state.
+constexpr int kGdnCols = 32;
+constexpr int kWStride = 132;   // fp32 row stride of W in shared memory (bank spread)
+constexpr int kQStride = 136;   // bf16 row stride of q in shared memory
+constexpr int kGdnStateSmem = 128 * kGdnCols * 4 + kGC * kWStride * 4 + kGC * kQStride * 2 +
+                              kGC * 128 * 2 + 2 * kGC * kGdnCols * 4 + 4 * kGC * 4;
+
+__global__ void __launch_bounds__(256) gdn_chunk_state_kernel(const GatedDeltaParams p,
+                                                              LinearAttnBatch bt,
+                                                              GdnChunkScratch cs) {
+  pdl_trigger();
+  pdl_wait();
+  const int b = blockIdx.x, h = blockIdx.y, cg = blockIdx.z;
+  const int tid = threadIdx.x, ty = tid >> 3, tx = tid & 7;
+  const int n = bt.q_start[b + 1] - bt.q_start[b];
+  if (n == 0) return;
+  const int ctx = bt.seq_lens[b] - n;
+  extern __shared__ __align__(16) uint8_t ssm[];
+  float* sS = reinterpret_cast<float*>(ssm);                 // [128][32]
+  float* sW = sS + 128 * kGdnCols;                            // [64][132]
+  __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(sW + kGC * kWStride);  // [64][136]
+  __nv_bfloat16* sK = sQ + kGC * kQStride;                    // [64][128]
+  float* sU = reinterpret_cast<float*>(sK + kGC * 128);       // [64][32]
+  float* sD = sU + kGC * kGdnCols;                            // [64][32]
+  float* slg = sD + kGC * kGdnCols;                           // [64]
+  float* sqf = slg + kGC;                                     // [64] gamma_t * |q|^-1 * dk^-1/2
+  float* skf = sqf + kGC;                                     // [64] |k|^-1 * e^{lg_L - lg_t}
+  float* sik = skf + kGC;                                     // [64] |k|^-1
+  float* S = p.state + (long long)bt.slots[b] * p.state_slot_stride + (long long)h * 128 * 128 +
+             cg * kGdnCols;
+  for (int i = tid; i < 128 * kGdnCols / 4; i += 256) {
+    const int r = i >> 3, c4 = i & 7;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (ctx > 0) v = *reinterpret_cast<const float4*>(S + (long long)r * 128 + c4 * 4);
+    *reinterpret_cast<float4*>(sS + r * kGdnCols + c4 * 4) = v;
+  }
+  const int kh = h / (p.Hv / p.Hk);
+  const float qscale = rsqrtf(128.f);
+  const int c0 = cs.seq_chunk0[b], c1 = cs.seq_chunk0[b + 1];
+  for (int c = c0; c < c1; ++c) {
+    const int4 ch = cs.chunks[c];
+    const int t0 = ch.x, L = ch.y;
+    // ---- stage the chunk
+    for (int i = tid; i < kGC * 32; i += 256) {  // W rows: 32 float4 each
+      const int r = i >> 5, c4 = i & 31;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (r < L) v = *reinterpret_cast<const float4*>(cs.W + ((long long)(t0 + r) * p.Hv + h) * 128 + c4 * 4);
+      *reinterpret_cast<float4*>(sW + r * kWStride + c4 * 4) = v;
+    }
+    for (int i = tid; i < kGC * 8; i += 256) {  // U columns of this CTA
+      const int r = i >> 3, c4 = i & 7;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (r < L)
+        v = *reinterpret_cast<const float4*>(cs.U + ((long long)(t0 + r) * p.Hv + h) * 128 +
+                                             cg * kGdnCols + c4 * 4);
+      *reinterpret_cast<float4*>(sU + r * kGdnCols + c4 * 4) = v;
+    }
+    for (int i = tid; i < kGC * 16; i += 256) {  // raw q and k rows of the key head
+      const int r = i >> 4, c8 = i & 15;
+      uint4 qv = make_uint4(0u, 0u, 0u, 0u), kv = qv;
+      if (r < L) {
+        const __nv_bfloat16* row = p.qkv + (long long)(t0 + r) * p.ld_qkv;
+        qv = *reinterpret_cast<const uint4*>(row + (long long)kh * 128 + c8 * 8);
+        kv = *reinterpret_cast<const uint4*>(row + (long long)(p.Hk + kh) * 128 + c8 * 8);
+      }
+      *reinterpret_cast<uint4*>(sQ + r * kQStride + c8 * 8) = qv;
+      *reinterpret_cast<uint4*>(sK + r * 128 + c8 * 8) = kv;
+    }
+    if (tid < kGC) {
+      float lg = 0.f, qf = 0.f, ik = 0.f;
+      if (tid < L) {
+        const long long t = t0 + tid;
+        lg = cs.lg[t * p.Hv + h];
+        const float4 gb = p.gb[t * p.Hv + h];
+        qf = __expf(lg) * gb.z * qscale;
+        ik = gb.w;
+      }
+      slg[tid] = lg;
+      sqf[tid] = qf;
+      sik[tid] = ik;
+    }
+    __syncthreads();
+    const float lgL = slg[L - 1];
+    if (tid < kGC) skf[tid] = tid < L ? sik[tid] * __expf(lgL - slg[tid]) : 0.f;
+    // ---- Delta = U - W S0 (rows 2ty, 2ty + 1; columns 4tx..4tx + 3)
+    {
+      float d[2][4];
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+        const float4 u = *reinterpret_cast<const float4*>(sU + (2 * ty + rr) * kGdnCols + tx * 4);
+        d[rr][0] = u.x; d[rr][1] = u.y; d[rr][2] = u.z; d[rr][3] = u.w;
+      }
+      const float* w0 = sW + (2 * ty) * kWStride;
+      const float* w1 = w0 + kWStride;
+#pragma unroll 8
+      for (int i = 0; i < 128; ++i) {
+        const float4 sv = *reinterpret_cast<const float4*>(sS + i * kGdnCols + tx * 4);
+        const float a0 = w0[i], a1 = w1[i];
+        d[0][0] -= a0 * sv.x; d[0][1] -= a0 * sv.y; d[0][2] -= a0 * sv.z; d[0][3] -= a0 * sv.w;
+        d[1][0] -= a1 * sv.x; d[1][1] -= a1 * sv.y; d[1][2] -= a1 * sv.z; d[1][3] -= a1 * sv.w;
+      }
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr)
+        *reinterpret_cast<float4*>(sD + (2 * ty + rr) * kGdnCols + tx * 4) =
+            make_float4(d[rr][0], d[rr][1], d[rr][2], d[rr][3]);
+    }
+    __syncthreads();
+    // ---- o_t = gamma_t q^_t S0 + sum_{s<=t} QKm[t, s] delta_s
+    {
+      float o[2][4];
+      const __nv_bfloat16* q0 = sQ + (2 * ty) * kQStride;
+      const __nv_bfloat16* q1 = q0 + kQStride;
+      float e0[4] = {0.f, 0.f, 0.f, 0.f}, e1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+      for (int i = 0; i < 128; i += 2) {
+        const float2 a0 = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(q0 + i));
+        const float2 a1 = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(q1 + i));
+        const float4 s0 = *reinterpret_cast<const float4*>(sS + i * kGdnCols + tx * 4);
+        const float4 s1 = *reinterpret_cast<const float4*>(sS + (i + 1) * kGdnCols + tx * 4);
+        e0[0] += a0.x * s0.x + a0.y * s1.x; e0[1] += a0.x * s0.y + a0.y * s1.y;
+        e0[2] += a0.x * s0.z + a0.y * s1.z; e0[3] += a0.x * s0.w + a0.y * s1.w;
+        e1[0] += a1.x * s0.x + a1.y * s1.x; e1[1] += a1.x * s0.y + a1.y * s1.y;
+        e1[2] += a1.x * s0.z + a1.y * s1.z; e1[3] += a1.x * s0.w + a1.y * s1.w;
+      }
+      const float f0 = sqf[2 * ty], f1 = sqf[2 * ty + 1];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        o[0][e] = e0[e] * f0;
+        o[1][e] = e1[e] * f1;
+      }
+      const float* qk0 = cs.QKm + ((long long)c * p.Hv + h) * (kGC * kGC) + (2 * ty) * kGC;
+      const float* qk1 = qk0 + kGC;
+      const int tmax = min(2 * ty + 1, L - 1);
+      for (int s2 = 0; s2 <= tmax; ++s2) {
+        const float4 dv = *reinterpret_cast<const float4*>(sD + s2 * kGdnCols + tx * 4);
+        const float m0 = __ldg(qk0 + s2), m1 = __ldg(qk1 + s2);
+        o[0][0] += m0 * dv.x; o[0][1] += m0 * dv.y; o[0][2] += m0 * dv.z; o[0][3] += m0 * dv.w;
+        o[1][0] += m1 * dv.x; o[1][1] += m1 * dv.y; o[1][2] += m1 * dv.z; o[1][3] += m1 * dv.w;
+      }
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+        const int t = 2 * ty + rr;
+        if (t < L)
+          *reinterpret_cast<uint2*>(p.out + (long long)(t0 + t) * p.ld_out + (long long)h * 128 +
+                                    cg * kGdnCols + tx * 4) =
+              make_uint2(pack_bf16x2(o[rr][0], o[rr][1]), pack_bf16x2(o[rr][2], o[rr][3]));
+      }
+    }
+    __syncthreads();
+    // ---- S = gamma_L S0 + sum_t k^_t e^{lg_L - lg_t} delta_t^T (rows 4ty..4ty+3)
+    {
+      const float gL = __expf(lgL);
+      float acc[4][4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const float4 sv = *reinterpret_cast<const float4*>(sS + (4 * ty + r) * kGdnCols + tx * 4);
+        acc[r][0] = gL * sv.x; acc[r][1] = gL * sv.y; acc[r][2] = gL * sv.z; acc[r][3] = gL * sv.w;
+      }
+      for (int t = 0; t < L; ++t) {
+        const uint2 kr = *reinterpret_cast<const uint2*>(sK + t * 128 + 4 * ty);
+        const float2 k01 = unpack_bf16x2(kr.x), k23 = unpack_bf16x2(kr.y);
+        const float f = skf[t];
+        const float4 dv = *reinterpret_cast<const float4*>(sD + t * kGdnCols + tx * 4);
+        const float kk[4] = {k01.x * f, k01.y * f, k23.x * f, k23.y * f};
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          acc[r][0] += kk[r] * dv.x; acc[r][1] += kk[r] * dv.y;
+          acc[r][2] += kk[r] * dv.z; acc[r][3] += kk[r] * dv.w;
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+        *reinterpret_cast<float4*>(sS + (4 * ty + r) * kGdnCols + tx * 4) =
+            make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+    }
+    __syncthreads();
+  }
+  for (int i = tid; i < 128 * kGdnCols / 4; i += 256) {
+    const int r = i >> 3, c4 = i & 7;
+    *reinterpret_cast<float4*>(S + (long long)r * 128 + c4 * 4) =
+        *reinterpret_cast<const float4*>(sS + r * kGdnCols + c4 * 4);
+  }
+}
+
 void causal_conv1d_launch(const __nv_bfloat16* x, long long ldx, int C, const __nv_bfloat16* w,
                           int K, const LinearAttnBatch& b, __nv_bfloat16* state,
                           long long state_slot_stride, __nv_bfloat16* y, long long ldy,
@@ -297,6 +682,36 @@ void gated_delta_rule_launch(const GatedDeltaParams& p, const LinearAttnBatch& b
   if (rows > 0)
     launch_pdl(gated_rmsnorm_kernel, dim3((rows + 7) / 8), dim3(256), 0, s, p.out, p.ld_out, p.z,
                p.ld_zab, p.norm_w, p.Hv, rows, p.eps);
+}
+
+void gated_delta_rule_chunked_launch(const GatedDeltaParams& p, const LinearAttnBatch& b,
+                                     const GdnChunkScratch& cs, cudaStream_t s) {
+  if (p.dk != 128 || p.dv != 128)
+    throw std::invalid_argument("gated_delta_rule: head dims must be 128");
+  if (p.Hv % p.Hk != 0) throw std::invalid_argument("gated_delta_rule: Hv % Hk != 0");
+  if (p.ld_qkv % 8 != 0 || p.ld_zab % 4 != 0 || p.ld_out % 4 != 0)
+    throw std::invalid_argument("gated_delta_rule: row strides must allow vector loads");
+  if (p.Hk > 64) throw std::invalid_argument("gated_delta_rule: at most 64 key heads per rank");
+  if (b.B == 0 || p.T == 0) return;
+  if (cs.max_chunks < p.T / kGC + b.B)
+    throw std::invalid_argument("gated_delta_rule: chunk scratch too small");
+  launch_pdl(gdn_prepare_kernel, dim3(p.T), dim3(256), 0, s, p);
+  launch_pdl(gdn_chunk_table_kernel, dim3(1), dim3(32), 0, s, b, cs.chunks, cs.seq_chunk0);
+  {
+    static std::atomic<uint64_t> configured{0};
+    set_max_dynamic_smem_once(gdn_chunk_prep_kernel, kGdnPrepSmem, configured);
+    launch_pdl(gdn_chunk_prep_kernel, dim3(cs.max_chunks, p.Hv), dim3(256), kGdnPrepSmem, s, p, cs,
+               b.B);
+  }
+  {
+    static std::atomic<uint64_t> configured{0};
+    set_max_dynamic_smem_once(gdn_chunk_state_kernel, kGdnStateSmem, configured);
+    launch_pdl(gdn_chunk_state_kernel, dim3(b.B, p.Hv, 128 / kGdnCols), dim3(256), kGdnStateSmem,
+               s, p, b, cs);
+  }
+  const int rows = p.T * p.Hv;
+  launch_pdl(gated_rmsnorm_kernel, dim3((rows + 7) / 8), dim3(256), 0, s, p.out, p.ld_out, p.z,
+             p.ld_zab, p.norm_w, p.Hv, rows, p.eps);
 }
 
 void sigmoid_gate_mul_launch(__nv_bfloat16* x, long long ldx, const __nv_bfloat16* gate,

@@ -50,6 +50,22 @@ struct GatedDeltaParams {
 // per-head gated RMSNorm out = rmsnorm(o) * w * silu(z).
 void gated_delta_rule_launch(const GatedDeltaParams& p, const LinearAttnBatch& b, cudaStream_t s);
 
+// Chunked (WY) form of the same rule for prefill-sized steps: tokens of each sequence are cut
+// into chunks of 64; a parallel pass solves the intra-chunk triangular system per (chunk,
+// value head) and a sequential pass per (sequence, value head, 32 value columns) carries the
+// fp32 state across the chunks.  Scratch (device memory the caller provides):
+struct GdnChunkScratch {
+  float* W;           // [T, Hv, dk]   (I + A)^-1 diag(beta gamma) K^
+  float* U;           // [T, Hv, dv]   (I + A)^-1 diag(beta) V
+  float* QKm;         // [max_chunks, Hv, 64, 64]  decay-masked Q^ K^T (s <= t)
+  float* lg;          // [T, Hv]       log of the cumulative decay from the chunk start
+  int4* chunks;       // [max_chunks]  (first token, length, sequence, -)
+  int* seq_chunk0;    // [B + 1]       first chunk of each sequence; [B] = chunk count
+  int max_chunks;     // >= T / 64 + B
+};
+void gated_delta_rule_chunked_launch(const GatedDeltaParams& p, const LinearAttnBatch& b,
+                                     const GdnChunkScratch& s, cudaStream_t stream);
+
 // x[t, i] *= sigmoid(gate[t, i]) for i < n.
 void sigmoid_gate_mul_launch(__nv_bfloat16* x, long long ldx, const __nv_bfloat16* gate,
                              long long ldg, int T, int n, cudaStream_t s);

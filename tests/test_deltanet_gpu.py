@@ -47,8 +47,9 @@ def test_causal_conv1d(cuda_device, K):
     assert _rel_err(state.cpu(), st_ref) < 1e-2
 
 
+@pytest.mark.parametrize("mode", ["recurrent", "chunked"])
 @pytest.mark.parametrize("Hk,Hv", [(2, 4), (4, 4)])
-def test_gated_delta_rule(cuda_device, Hk, Hv):
+def test_gated_delta_rule(cuda_device, Hk, Hv, mode):
     dk = dv = 128
     q_lens, ctx = [1, 64, 7, 130, 1, 1], [20, 0, 5, 0, 0, 300]
     qs, sl, slots = _batch(q_lens, ctx, cuda_device)
@@ -63,11 +64,13 @@ def test_gated_delta_rule(cuda_device, Hk, Hv):
     st_ref = state.cpu().clone()
     out = torch.empty(T, Hv * dv, device=cuda_device, dtype=torch.bfloat16)
     for _ in range(2):  # the second call continues from the updated state
-        DN.gated_delta_rule(qkv, z, a, b, A_log, dt_bias, nw, 1e-6, qs, sl, slots, state, out, Hk, Hv)
+        DN.gated_delta_rule(qkv, z, a, b, A_log, dt_bias, nw, 1e-6, qs, sl, slots, state, out, Hk, Hv,
+                            mode=mode)
         ref = DN.gated_delta_rule_ref(qkv.cpu(), z.cpu(), a.cpu(), b.cpu(), A_log.cpu(), dt_bias.cpu(),
                                       nw.cpu(), 1e-6, qs.cpu(), sl.cpu(), slots.cpu(), st_ref, Hk, Hv)
         assert _rel_err(out.cpu(), ref) < 2e-2
-        assert _rel_err(state.cpu(), st_ref) < 1e-3
+        # the chunked form multiplies bf16-rounded unit q / k on the tensor cores
+        assert _rel_err(state.cpu(), st_ref) < (1e-3 if mode == "recurrent" else 5e-3)
         sl = sl + torch.tensor(q_lens, dtype=torch.int32, device=cuda_device)
 
 
@@ -77,3 +80,28 @@ def test_sigmoid_gate_mul(cuda_device):
     ref = x.float() * torch.sigmoid(g.float())
     DN.sigmoid_gate_mul(x, g)
     assert _rel_err(x, ref) < 1e-2
+
+
+def test_gated_delta_rule_chunked_long(cuda_device):
+    """Many chunks per sequence (state carried across 16 chunks) against the recurrent kernel,
+    with a continuing sequence and a ragged last chunk; Qwen3.6-like head ratio."""
+    Hk, Hv, dk = 4, 8, 128
+    q_lens, ctx = [1000, 777, 1], [0, 50, 9]
+    qs, sl, slots = _batch(q_lens, ctx, cuda_device)
+    T = sum(q_lens)
+    qkv = torch.randn(T, 2 * Hk * dk + Hv * dk, device=cuda_device).to(torch.bfloat16)
+    zab = torch.randn(T, Hv * dk + 2 * Hv, device=cuda_device).to(torch.bfloat16)
+    z, b, a = zab[:, :Hv * dk], zab[:, Hv * dk:Hv * dk + Hv], zab[:, Hv * dk + Hv:]
+    A_log = torch.rand(Hv, device=cuda_device).mul(3).add(0.1).log()
+    dt_bias = torch.randn(Hv, device=cuda_device) * 0.5 - 2.0  # slow decays: long memory
+    nw = (1 + 0.1 * torch.randn(dk, device=cuda_device)).to(torch.bfloat16)
+    state = torch.randn(20, Hv, dk, dk, device=cuda_device) * 0.1
+    st_rec = state.clone()
+    out = torch.empty(T, Hv * dk, device=cuda_device, dtype=torch.bfloat16)
+    out_rec = torch.empty_like(out)
+    DN.gated_delta_rule(qkv, z, a, b, A_log, dt_bias, nw, 1e-6, qs, sl, slots, state, out, Hk, Hv,
+                        mode="chunked")
+    DN.gated_delta_rule(qkv, z, a, b, A_log, dt_bias, nw, 1e-6, qs, sl, slots, st_rec, out_rec, Hk,
+                        Hv, mode="recurrent")
+    assert _rel_err(out, out_rec) < 2e-2
+    assert _rel_err(state, st_rec) < 1e-2

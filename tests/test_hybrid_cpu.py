@@ -67,3 +67,45 @@ def test_conv1d_ref_matches_full_sequence():
     a = DN.causal_conv1d_ref(x[:7], w, torch.tensor([0, 7]), torch.tensor([7]), slots, state)
     b = DN.causal_conv1d_ref(x[7:], w, torch.tensor([0, 3]), torch.tensor([10]), slots, state)
     assert torch.allclose(torch.cat([a, b]), full, atol=1e-5)
+
+
+def test_chunked_delta_rule_restatement_matches_recurrence():
+    """The chunked (WY) form computed by the prefill kernels, restated in torch, equals the
+    token-by-token recurrence: outputs and carried state, fresh and continuing sequences."""
+    import torch.nn.functional as F
+
+    from vllm_neuron_b200.ops import deltanet as DN
+
+    g = torch.Generator().manual_seed(0)
+    Hk, Hv, dk = 2, 4, 128
+    q_lens, ctx = [150, 1, 64, 65, 3], [0, 10, 70, 0, 5]
+    T = sum(q_lens)
+    qkv = torch.randn(T, 2 * Hk * dk + Hv * dk, generator=g)
+    a, b = torch.randn(T, Hv, generator=g), torch.randn(T, Hv, generator=g)
+    A_log, dt_bias = torch.randn(Hv, generator=g) * 0.5, torch.randn(Hv, generator=g) * 0.3
+    qs = torch.tensor([0] + list(torch.tensor(q_lens).cumsum(0)), dtype=torch.int32)
+    sl = torch.tensor([c + q for c, q in zip(ctx, q_lens)], dtype=torch.int32)
+    slots = torch.tensor([3, 0, 2, 1, 4], dtype=torch.int32)
+    st_rec = torch.randn(5, Hv, dk, dk, generator=g) * 0.1
+    st_chk = st_rec.clone()
+    # recurrence with an identity "norm" (z -> silu^-1 unneeded: compare pre-norm outputs)
+    q = qkv[:, :Hk * dk].view(T, Hk, dk).repeat_interleave(Hv // Hk, 1)
+    k = qkv[:, Hk * dk:2 * Hk * dk].view(T, Hk, dk).repeat_interleave(Hv // Hk, 1)
+    v = qkv[:, 2 * Hk * dk:].view(T, Hv, dk)
+    q = q * torch.rsqrt((q * q).sum(-1, keepdim=True) + 1e-6) * dk ** -0.5
+    k = k * torch.rsqrt((k * k).sum(-1, keepdim=True) + 1e-6)
+    gt = torch.exp(-A_log.exp() * F.softplus(a + dt_bias))
+    beta = torch.sigmoid(b)
+    o_rec = torch.zeros(T, Hv, dk)
+    for bi in range(len(q_lens)):
+        t0, t1 = int(qs[bi]), int(qs[bi + 1])
+        S = st_rec[slots[bi]].clone() if ctx[bi] > 0 else torch.zeros(Hv, dk, dk)
+        for t in range(t0, t1):
+            S = S * gt[t][:, None, None]
+            d = (v[t] - torch.einsum("hkv,hk->hv", S, k[t])) * beta[t][:, None]
+            S = S + k[t][:, :, None] * d[:, None, :]
+            o_rec[t] = torch.einsum("hkv,hk->hv", S, q[t])
+        st_rec[slots[bi]].copy_(S)
+    o_chk = DN.gated_delta_rule_chunked_ref(qkv, a, b, A_log, dt_bias, qs, sl, slots, st_chk, Hk, Hv)
+    assert ((o_chk - o_rec).norm() / o_rec.norm()).item() < 1e-5
+    assert ((st_chk - st_rec).norm() / st_rec.norm()).item() < 1e-5
