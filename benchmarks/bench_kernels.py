@@ -90,11 +90,14 @@ def bench_gemms(tp: int):
 def bench_decode_attention(tp: int):
     Hq, Hkv, D, bs = 32 // tp, max(1, 8 // tp), 128, 16
     rows = []
-    for B, ctx in ((64, 1152), (64, 4096), (16, 8192)):
+    for B, ctx, kvdt in ((64, 1152, "bf16"), (64, 4096, "bf16"), (16, 8192, "bf16"),
+                         (64, 1152, "fp8"), (64, 4096, "fp8")):
         nblk = (ctx + bs - 1) // bs
         nb = B * nblk + 1
         kc = torch.randn(nb, Hkv, bs, D, device="cuda", dtype=torch.bfloat16)
         vc = torch.randn_like(kc)
+        if kvdt == "fp8":
+            kc, vc = kc.to(torch.float8_e4m3fn), vc.to(torch.float8_e4m3fn)
         bt = (torch.randperm(nb - 1, device="cuda")[: B * nblk] + 1).view(B, nblk).to(torch.int32)
         sl = torch.full((B,), ctx, dtype=torch.int32, device="cuda")
         qs = torch.arange(B + 1, dtype=torch.int32, device="cuda")
@@ -107,8 +110,8 @@ def bench_decode_attention(tp: int):
         fn = lambda: ops.paged_attention(q, kc, vc, bt, sl, qs, work, True, w.num_splits,
                                          1 / math.sqrt(D), out=out, part_o=part_o, part_lse=part_l)
         t = timeit(fn)
-        kv_bytes = 2 * B * ctx * Hkv * D * 2
-        rows.append({"op": "decode_attention", "B": B, "ctx": ctx, "Hq": Hq, "Hkv": Hkv,
+        kv_bytes = 2 * B * ctx * Hkv * D * kc.element_size()
+        rows.append({"op": "decode_attention", "kv": kvdt, "B": B, "ctx": ctx, "Hq": Hq, "Hkv": Hkv,
                      "splits": w.num_splits, "ms": t, "gbs": kv_bytes / t / 1e6})
         print(json.dumps(rows[-1]), flush=True)
     return rows
