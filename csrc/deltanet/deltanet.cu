@@ -449,9 +449,17 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(const GatedDeltaPar
         r = sbeta[t] * __bfloat162float(vcol[(long long)t * p.ld_qkv]);
       }
     }
+    // four independent partial sums break the dependent FMA chain
+    float r1 = 0.f, r2 = 0.f, r3 = 0.f;
 #pragma unroll
-    for (int s2 = 0; s2 < t; ++s2) r = fmaf(-sKK[t * 65 + s2], x[s2], r);
-    x[t] = r;
+    for (int s2 = 0; s2 < t; ++s2) {
+      const float m = sKK[t * 65 + s2] * x[s2];
+      if ((s2 & 3) == 0) r -= m;
+      else if ((s2 & 3) == 1) r1 -= m;
+      else if ((s2 & 3) == 2) r2 -= m;
+      else r3 -= m;
+    }
+    x[t] = (r + r1) + (r2 + r3);
   }
   float* dst = (isw ? cs.W : cs.U) + ((long long)t0 * p.Hv + h) * 128 + (j & 127);
 #pragma unroll
@@ -461,13 +469,34 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(const GatedDeltaPar
 }
 
 // grid (B, Hv, 4), 256 threads: 32 value columns of one (sequence, value head), all chunks
-// of the sequence in order.  Thread (ty = tid / 8, tx = tid % 8) owns value columns 4tx..4tx+3
-// and rows 2ty, 2ty+1 of the chunk outputs, or rows 4ty..4ty+3 of the state.
+// of the sequence in order, the chunk products on the tensor cores (mma m16n8k8 tf32, fp32
+// accumulation; the state itself stays fp32 in shared memory).  Per chunk, 8 warps:
+//   Delta[64 x 32] = U - W S0                 warp (m tile w % 4, 16 columns w / 4), k = 128
+//   O[64 x 32]     = qf * (Q S0) + QKm Delta  same tiling, k = 128 and k = 64 (lower blocks)
+//   S[128 x 32]    = gamma_L S0 + K^T (f * Delta)   warp = 16 state rows x 32 columns, k = 64
 constexpr int kGdnCols = 32;
-constexpr int kWStride = 132;   // fp32 row stride of W in shared memory (bank spread)
-constexpr int kQStride = 136;   // bf16 row stride of q in shared memory
-constexpr int kGdnStateSmem = 128 * kGdnCols * 4 + kGC * kWStride * 4 + kGC * kQStride * 2 +
-                              kGC * 128 * 2 + 2 * kGC * kGdnCols * 4 + 4 * kGC * 4;
+constexpr int kSS = 36;        // fp32 row stride of S / Delta (conflict-free B fragments)
+constexpr int kWStride = 132;  // fp32 row stride of W (conflict-free A fragments)
+constexpr int kQStride = 136;  // bf16 row stride of q and k
+constexpr int kGdnStateSmem = 128 * kSS * 4 + kGC * kWStride * 4 + 2 * kGC * kQStride * 2 +
+                              kGC * kSS * 4 + 4 * kGC * 4;
+
+namespace {
+__device__ __forceinline__ uint32_t tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ void mma_tf32(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+      "{%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ float bf(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+}  // namespace
 
 __global__ void __launch_bounds__(256) gdn_chunk_state_kernel(const GatedDeltaParams p,
                                                               LinearAttnBatch bt,
@@ -475,51 +504,44 @@ __global__ void __launch_bounds__(256) gdn_chunk_state_kernel(const GatedDeltaPa
   pdl_trigger();
   pdl_wait();
   const int b = blockIdx.x, h = blockIdx.y, cg = blockIdx.z;
-  const int tid = threadIdx.x, ty = tid >> 3, tx = tid & 7;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t4 = lane & 3;
   const int n = bt.q_start[b + 1] - bt.q_start[b];
   if (n == 0) return;
   const int ctx = bt.seq_lens[b] - n;
   extern __shared__ __align__(16) uint8_t ssm[];
-  float* sS = reinterpret_cast<float*>(ssm);                 // [128][32]
-  float* sW = sS + 128 * kGdnCols;                            // [64][132]
+  float* sS = reinterpret_cast<float*>(ssm);                                  // [128][36]
+  float* sW = sS + 128 * kSS;                                                  // [64][132]
   __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(sW + kGC * kWStride);  // [64][136]
-  __nv_bfloat16* sK = sQ + kGC * kQStride;                    // [64][128]
-  float* sU = reinterpret_cast<float*>(sK + kGC * 128);       // [64][32]
-  float* sD = sU + kGC * kGdnCols;                            // [64][32]
-  float* slg = sD + kGC * kGdnCols;                           // [64]
-  float* sqf = slg + kGC;                                     // [64] gamma_t * |q|^-1 * dk^-1/2
-  float* skf = sqf + kGC;                                     // [64] |k|^-1 * e^{lg_L - lg_t}
-  float* sik = skf + kGC;                                     // [64] |k|^-1
+  __nv_bfloat16* sK = sQ + kGC * kQStride;                                     // [64][136]
+  float* sD = reinterpret_cast<float*>(sK + kGC * kQStride);                   // [64][36]
+  float* slg = sD + kGC * kSS;   // [64] cumulative log decay
+  float* sqf = slg + kGC;        // [64] gamma_t |q|^-1 dk^-1/2
+  float* skf = sqf + kGC;        // [64] |k|^-1 e^{lg_L - lg_t}
+  float* sik = skf + kGC;        // [64] |k|^-1
   float* S = p.state + (long long)bt.slots[b] * p.state_slot_stride + (long long)h * 128 * 128 +
              cg * kGdnCols;
   for (int i = tid; i < 128 * kGdnCols / 4; i += 256) {
     const int r = i >> 3, c4 = i & 7;
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
     if (ctx > 0) v = *reinterpret_cast<const float4*>(S + (long long)r * 128 + c4 * 4);
-    *reinterpret_cast<float4*>(sS + r * kGdnCols + c4 * 4) = v;
+    *reinterpret_cast<float4*>(sS + r * kSS + c4 * 4) = v;
   }
   const int kh = h / (p.Hv / p.Hk);
   const float qscale = rsqrtf(128.f);
+  const int mt = warp & 3, nh = warp >> 2;  // chunk-output tiling
   const int c0 = cs.seq_chunk0[b], c1 = cs.seq_chunk0[b + 1];
   for (int c = c0; c < c1; ++c) {
     const int4 ch = cs.chunks[c];
     const int t0 = ch.x, L = ch.y;
-    // ---- stage the chunk
-    for (int i = tid; i < kGC * 32; i += 256) {  // W rows: 32 float4 each
+    // ---- stage the chunk (rows past L are zero)
+    for (int i = tid; i < kGC * 32; i += 256) {
       const int r = i >> 5, c4 = i & 31;
       float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
       if (r < L) v = *reinterpret_cast<const float4*>(cs.W + ((long long)(t0 + r) * p.Hv + h) * 128 + c4 * 4);
       *reinterpret_cast<float4*>(sW + r * kWStride + c4 * 4) = v;
     }
-    for (int i = tid; i < kGC * 8; i += 256) {  // U columns of this CTA
-      const int r = i >> 3, c4 = i & 7;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (r < L)
-        v = *reinterpret_cast<const float4*>(cs.U + ((long long)(t0 + r) * p.Hv + h) * 128 +
-                                             cg * kGdnCols + c4 * 4);
-      *reinterpret_cast<float4*>(sU + r * kGdnCols + c4 * 4) = v;
-    }
-    for (int i = tid; i < kGC * 16; i += 256) {  // raw q and k rows of the key head
+    for (int i = tid; i < kGC * 16; i += 256) {
       const int r = i >> 4, c8 = i & 15;
       uint4 qv = make_uint4(0u, 0u, 0u, 0u), kv = qv;
       if (r < L) {
@@ -528,7 +550,7 @@ __global__ void __launch_bounds__(256) gdn_chunk_state_kernel(const GatedDeltaPa
         kv = *reinterpret_cast<const uint4*>(row + (long long)(p.Hk + kh) * 128 + c8 * 8);
       }
       *reinterpret_cast<uint4*>(sQ + r * kQStride + c8 * 8) = qv;
-      *reinterpret_cast<uint4*>(sK + r * 128 + c8 * 8) = kv;
+      *reinterpret_cast<uint4*>(sK + r * kQStride + c8 * 8) = kv;
     }
     if (tid < kGC) {
       float lg = 0.f, qf = 0.f, ik = 0.f;
@@ -546,103 +568,114 @@ __global__ void __launch_bounds__(256) gdn_chunk_state_kernel(const GatedDeltaPa
     __syncthreads();
     const float lgL = slg[L - 1];
     if (tid < kGC) skf[tid] = tid < L ? sik[tid] * __expf(lgL - slg[tid]) : 0.f;
-    // ---- Delta = U - W S0 (rows 2ty, 2ty + 1; columns 4tx..4tx + 3)
+    const int r0 = mt * 16 + g, r1 = r0 + 8;  // chunk rows of this lane's accumulators
+    // ---- Delta = U - W S0
     {
-      float d[2][4];
+      float acc[2][4];
 #pragma unroll
-      for (int rr = 0; rr < 2; ++rr) {
-        const float4 u = *reinterpret_cast<const float4*>(sU + (2 * ty + rr) * kGdnCols + tx * 4);
-        d[rr][0] = u.x; d[rr][1] = u.y; d[rr][2] = u.z; d[rr][3] = u.w;
-      }
-      const float* w0 = sW + (2 * ty) * kWStride;
-      const float* w1 = w0 + kWStride;
-#pragma unroll 8
-      for (int i = 0; i < 128; ++i) {
-        const float4 sv = *reinterpret_cast<const float4*>(sS + i * kGdnCols + tx * 4);
-        const float a0 = w0[i], a1 = w1[i];
-        d[0][0] -= a0 * sv.x; d[0][1] -= a0 * sv.y; d[0][2] -= a0 * sv.z; d[0][3] -= a0 * sv.w;
-        d[1][0] -= a1 * sv.x; d[1][1] -= a1 * sv.y; d[1][2] -= a1 * sv.z; d[1][3] -= a1 * sv.w;
-      }
-#pragma unroll
-      for (int rr = 0; rr < 2; ++rr)
-        *reinterpret_cast<float4*>(sD + (2 * ty + rr) * kGdnCols + tx * 4) =
-            make_float4(d[rr][0], d[rr][1], d[rr][2], d[rr][3]);
-    }
-    __syncthreads();
-    // ---- o_t = gamma_t q^_t S0 + sum_{s<=t} QKm[t, s] delta_s
-    {
-      float o[2][4];
-      const __nv_bfloat16* q0 = sQ + (2 * ty) * kQStride;
-      const __nv_bfloat16* q1 = q0 + kQStride;
-      float e0[4] = {0.f, 0.f, 0.f, 0.f}, e1[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int j = 0; j < 2; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
 #pragma unroll 4
-      for (int i = 0; i < 128; i += 2) {
-        const float2 a0 = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(q0 + i));
-        const float2 a1 = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(q1 + i));
-        const float4 s0 = *reinterpret_cast<const float4*>(sS + i * kGdnCols + tx * 4);
-        const float4 s1 = *reinterpret_cast<const float4*>(sS + (i + 1) * kGdnCols + tx * 4);
-        e0[0] += a0.x * s0.x + a0.y * s1.x; e0[1] += a0.x * s0.y + a0.y * s1.y;
-        e0[2] += a0.x * s0.z + a0.y * s1.z; e0[3] += a0.x * s0.w + a0.y * s1.w;
-        e1[0] += a1.x * s0.x + a1.y * s1.x; e1[1] += a1.x * s0.y + a1.y * s1.y;
-        e1[2] += a1.x * s0.z + a1.y * s1.z; e1[3] += a1.x * s0.w + a1.y * s1.w;
-      }
-      const float f0 = sqf[2 * ty], f1 = sqf[2 * ty + 1];
+      for (int ks = 0; ks < 16; ++ks) {
+        const int kc = ks * 8 + t4;
+        const uint32_t a0 = tf32(sW[r0 * kWStride + kc]), a1 = tf32(sW[r1 * kWStride + kc]);
+        const uint32_t a2 = tf32(sW[r0 * kWStride + kc + 4]), a3 = tf32(sW[r1 * kWStride + kc + 4]);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        o[0][e] = e0[e] * f0;
-        o[1][e] = e1[e] * f1;
-      }
-      const float* qk0 = cs.QKm + ((long long)c * p.Hv + h) * (kGC * kGC) + (2 * ty) * kGC;
-      const float* qk1 = qk0 + kGC;
-      const int tmax = min(2 * ty + 1, L - 1);
-      for (int s2 = 0; s2 <= tmax; ++s2) {
-        const float4 dv = *reinterpret_cast<const float4*>(sD + s2 * kGdnCols + tx * 4);
-        const float m0 = __ldg(qk0 + s2), m1 = __ldg(qk1 + s2);
-        o[0][0] += m0 * dv.x; o[0][1] += m0 * dv.y; o[0][2] += m0 * dv.z; o[0][3] += m0 * dv.w;
-        o[1][0] += m1 * dv.x; o[1][1] += m1 * dv.y; o[1][2] += m1 * dv.z; o[1][3] += m1 * dv.w;
-      }
-#pragma unroll
-      for (int rr = 0; rr < 2; ++rr) {
-        const int t = 2 * ty + rr;
-        if (t < L)
-          *reinterpret_cast<uint2*>(p.out + (long long)(t0 + t) * p.ld_out + (long long)h * 128 +
-                                    cg * kGdnCols + tx * 4) =
-              make_uint2(pack_bf16x2(o[rr][0], o[rr][1]), pack_bf16x2(o[rr][2], o[rr][3]));
-      }
-    }
-    __syncthreads();
-    // ---- S = gamma_L S0 + sum_t k^_t e^{lg_L - lg_t} delta_t^T (rows 4ty..4ty+3)
-    {
-      const float gL = __expf(lgL);
-      float acc[4][4];
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const float4 sv = *reinterpret_cast<const float4*>(sS + (4 * ty + r) * kGdnCols + tx * 4);
-        acc[r][0] = gL * sv.x; acc[r][1] = gL * sv.y; acc[r][2] = gL * sv.z; acc[r][3] = gL * sv.w;
-      }
-      for (int t = 0; t < L; ++t) {
-        const uint2 kr = *reinterpret_cast<const uint2*>(sK + t * 128 + 4 * ty);
-        const float2 k01 = unpack_bf16x2(kr.x), k23 = unpack_bf16x2(kr.y);
-        const float f = skf[t];
-        const float4 dv = *reinterpret_cast<const float4*>(sD + t * kGdnCols + tx * 4);
-        const float kk[4] = {k01.x * f, k01.y * f, k23.x * f, k23.y * f};
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-          acc[r][0] += kk[r] * dv.x; acc[r][1] += kk[r] * dv.y;
-          acc[r][2] += kk[r] * dv.z; acc[r][3] += kk[r] * dv.w;
+        for (int j = 0; j < 2; ++j) {
+          const int col = nh * 16 + j * 8 + g;
+          mma_tf32(acc[j], a0, a1, a2, a3, tf32(sS[kc * kSS + col]), tf32(sS[(kc + 4) * kSS + col]));
         }
       }
 #pragma unroll
-      for (int r = 0; r < 4; ++r)
-        *reinterpret_cast<float4*>(sS + (4 * ty + r) * kGdnCols + tx * 4) =
-            make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+      for (int j = 0; j < 2; ++j) {
+        const int col = nh * 16 + j * 8 + 2 * t4;
+        float2 u0 = make_float2(0.f, 0.f), u1 = u0;
+        if (r0 < L) u0 = *reinterpret_cast<const float2*>(cs.U + ((long long)(t0 + r0) * p.Hv + h) * 128 + cg * kGdnCols + col);
+        if (r1 < L) u1 = *reinterpret_cast<const float2*>(cs.U + ((long long)(t0 + r1) * p.Hv + h) * 128 + cg * kGdnCols + col);
+        *reinterpret_cast<float2*>(sD + r0 * kSS + col) = make_float2(u0.x - acc[j][0], u0.y - acc[j][1]);
+        *reinterpret_cast<float2*>(sD + r1 * kSS + col) = make_float2(u1.x - acc[j][2], u1.y - acc[j][3]);
+      }
+    }
+    __syncthreads();
+    // ---- O = qf * (Q S0) + QKm Delta
+    {
+      float acc[2][4];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+#pragma unroll 4
+      for (int ks = 0; ks < 16; ++ks) {
+        const int kc = ks * 8 + t4;
+        const uint32_t a0 = tf32(bf(sQ + r0 * kQStride + kc)), a1 = tf32(bf(sQ + r1 * kQStride + kc));
+        const uint32_t a2 = tf32(bf(sQ + r0 * kQStride + kc + 4)), a3 = tf32(bf(sQ + r1 * kQStride + kc + 4));
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int col = nh * 16 + j * 8 + g;
+          mma_tf32(acc[j], a0, a1, a2, a3, tf32(sS[kc * kSS + col]), tf32(sS[(kc + 4) * kSS + col]));
+        }
+      }
+      const float f0 = sqf[r0], f1 = sqf[r1];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        acc[j][0] *= f0; acc[j][1] *= f0; acc[j][2] *= f1; acc[j][3] *= f1;
+      }
+      // QKm is lower triangular: k steps past this m tile's last row contribute nothing
+      const float* qk = cs.QKm + ((long long)c * p.Hv + h) * (kGC * kGC);
+      for (int ks = 0; ks < 2 * mt + 2; ++ks) {
+        const int kc = ks * 8 + t4;
+        const uint32_t a0 = tf32(__ldg(qk + r0 * kGC + kc)), a1 = tf32(__ldg(qk + r1 * kGC + kc));
+        const uint32_t a2 = tf32(__ldg(qk + r0 * kGC + kc + 4)), a3 = tf32(__ldg(qk + r1 * kGC + kc + 4));
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int col = nh * 16 + j * 8 + g;
+          mma_tf32(acc[j], a0, a1, a2, a3, tf32(sD[kc * kSS + col]), tf32(sD[(kc + 4) * kSS + col]));
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int col = h * 128 + cg * kGdnCols + nh * 16 + j * 8 + 2 * t4;
+        if (r0 < L)
+          *reinterpret_cast<uint32_t*>(p.out + (long long)(t0 + r0) * p.ld_out + col) = pack_bf16x2(acc[j][0], acc[j][1]);
+        if (r1 < L)
+          *reinterpret_cast<uint32_t*>(p.out + (long long)(t0 + r1) * p.ld_out + col) = pack_bf16x2(acc[j][2], acc[j][3]);
+      }
+    }
+    __syncthreads();
+    // ---- S = gamma_L S0 + K^T (f * Delta): warp owns state rows 16w..16w+15, all 32 columns
+    {
+      const float gL = __expf(lgL);
+      const int s0 = warp * 16 + g, s1 = s0 + 8;
+      float acc[4][4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int col = j * 8 + 2 * t4;
+        const float2 x0 = *reinterpret_cast<const float2*>(sS + s0 * kSS + col);
+        const float2 x1 = *reinterpret_cast<const float2*>(sS + s1 * kSS + col);
+        acc[j][0] = gL * x0.x; acc[j][1] = gL * x0.y; acc[j][2] = gL * x1.x; acc[j][3] = gL * x1.y;
+      }
+      const int ksteps = (L + 7) >> 3;
+      for (int ks = 0; ks < ksteps; ++ks) {
+        const int kt = ks * 8 + t4;  // token of a0 / b0
+        const uint32_t a0 = tf32(bf(sK + kt * kQStride + s0)), a1 = tf32(bf(sK + kt * kQStride + s1));
+        const uint32_t a2 = tf32(bf(sK + (kt + 4) * kQStride + s0)), a3 = tf32(bf(sK + (kt + 4) * kQStride + s1));
+        const float fa = skf[kt], fb = skf[kt + 4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int col = j * 8 + g;
+          mma_tf32(acc[j], a0, a1, a2, a3, tf32(fa * sD[kt * kSS + col]), tf32(fb * sD[(kt + 4) * kSS + col]));
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int col = j * 8 + 2 * t4;
+        *reinterpret_cast<float2*>(sS + s0 * kSS + col) = make_float2(acc[j][0], acc[j][1]);
+        *reinterpret_cast<float2*>(sS + s1 * kSS + col) = make_float2(acc[j][2], acc[j][3]);
+      }
     }
     __syncthreads();
   }
   for (int i = tid; i < 128 * kGdnCols / 4; i += 256) {
     const int r = i >> 3, c4 = i & 7;
     *reinterpret_cast<float4*>(S + (long long)r * 128 + c4 * 4) =
-        *reinterpret_cast<const float4*>(sS + r * kGdnCols + c4 * 4);
+        *reinterpret_cast<const float4*>(sS + r * kSS + c4 * 4);
   }
 }
 
