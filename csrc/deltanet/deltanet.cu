@@ -317,8 +317,10 @@ __global__ void gdn_chunk_table_kernel(LinearAttnBatch bt, int4* chunks, int* se
   seq_chunk0[bt.B] = c;
 }
 
-// grid (max_chunks, Hv), 256 threads; dynamic smem = kGdnPrepSmem
-constexpr int kGdnPrepSmem = 2 * kGC * 128 * 2 + 2 * kGC * 65 * 4 + 2 * kGC * 4;
+// grid (max_chunks, Hv), 256 threads; dynamic smem = kGdnPrepSmem.  q^ and k^ are held as
+// bf16 pairs hi + lo (hi = bf16(x), lo = bf16(x - hi)); the products keep hi*hi + hi*lo + lo*hi,
+// about 16 mantissa bits, so the triangular system sees nearly fp32 dot products.
+constexpr int kGdnPrepSmem = 4 * kGC * 128 * 2 + 2 * kGC * 65 * 4 + 2 * kGC * 4;
 
 __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(const GatedDeltaParams p,
                                                              GdnChunkScratch cs, int B) {
@@ -331,9 +333,11 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(const GatedDeltaPar
   const int kh = h / (p.Hv / p.Hk);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   extern __shared__ __align__(128) uint8_t gsm[];
-  uint8_t* sq = gsm;                                   // q^ [64][128] bf16
-  uint8_t* sk = sq + kGC * 256;                        // k^ [64][128] bf16
-  float* sKK = reinterpret_cast<float*>(sk + kGC * 256);  // [64][65]: K^K^T, then A
+  uint8_t* sq = gsm;                                   // q^ hi [64][128] bf16
+  uint8_t* sk = sq + kGC * 256;                        // k^ hi
+  uint8_t* sql = sk + kGC * 256;                       // q^ lo
+  uint8_t* skl = sql + kGC * 256;                      // k^ lo
+  float* sKK = reinterpret_cast<float*>(skl + kGC * 256);  // [64][65]: K^K^T, then A
   float* sQK = sKK + kGC * 65;                          // [64][65]: Q^K^T
   float* slg = sQK + kGC * 65;                          // [64]
   float* sbeta = slg + kGC;                             // [64]
@@ -353,7 +357,7 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(const GatedDeltaPar
   const float qscale = rsqrtf(128.f);
   for (int i = tid; i < kGC * 16; i += 256) {
     const int r = i >> 4, cc = i & 15;
-    uint4 qo = make_uint4(0u, 0u, 0u, 0u), ko = qo;
+    uint4 qo = make_uint4(0u, 0u, 0u, 0u), ko = qo, qlo = qo, klo = qo;
     if (r < L) {
       const long long t = t0 + r;
       const float4 gb = p.gb[t * p.Hv + h];
@@ -361,19 +365,27 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(const GatedDeltaPar
       const uint4 qi = *reinterpret_cast<const uint4*>(row + (long long)kh * 128 + cc * 8);
       const uint4 ki = *reinterpret_cast<const uint4*>(row + (long long)(p.Hk + kh) * 128 + cc * 8);
       const uint32_t qw[4] = {qi.x, qi.y, qi.z, qi.w}, kw[4] = {ki.x, ki.y, ki.z, ki.w};
-      uint32_t qn[4], kn[4];
+      uint32_t qn[4], kn[4], ql[4], kl[4];
+      const float sq_ = gb.z * qscale;
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float2 fq = unpack_bf16x2(qw[e]), fk = unpack_bf16x2(kw[e]);
-        const float sq_ = gb.z * qscale;
-        qn[e] = pack_bf16x2(fq.x * sq_, fq.y * sq_);
-        kn[e] = pack_bf16x2(fk.x * gb.w, fk.y * gb.w);
+        const float q0 = fq.x * sq_, q1 = fq.y * sq_, k0 = fk.x * gb.w, k1 = fk.y * gb.w;
+        qn[e] = pack_bf16x2(q0, q1);
+        kn[e] = pack_bf16x2(k0, k1);
+        const float2 qh = unpack_bf16x2(qn[e]), kh2 = unpack_bf16x2(kn[e]);
+        ql[e] = pack_bf16x2(q0 - qh.x, q1 - qh.y);
+        kl[e] = pack_bf16x2(k0 - kh2.x, k1 - kh2.y);
       }
       qo = make_uint4(qn[0], qn[1], qn[2], qn[3]);
       ko = make_uint4(kn[0], kn[1], kn[2], kn[3]);
+      qlo = make_uint4(ql[0], ql[1], ql[2], ql[3]);
+      klo = make_uint4(kl[0], kl[1], kl[2], kl[3]);
     }
     *reinterpret_cast<uint4*>(sq + gdn_swz(r, cc)) = qo;
     *reinterpret_cast<uint4*>(sk + gdn_swz(r, cc)) = ko;
+    *reinterpret_cast<uint4*>(sql + gdn_swz(r, cc)) = qlo;
+    *reinterpret_cast<uint4*>(skl + gdn_swz(r, cc)) = klo;
   }
   __syncthreads();
   if (tid == 0) {  // inclusive prefix sum of the log decays
@@ -386,24 +398,32 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(const GatedDeltaPar
   // K^K^T (warps 0-3) and Q^K^T (warps 4-7): 16 rows x 64 columns per warp, k = 128
   {
     const uint8_t* sa = warp < 4 ? sk : sq;
+    const uint8_t* sal = warp < 4 ? skl : sql;
     float* dst = warp < 4 ? sKK : sQK;
     const int wrow = (warp & 3) * 16;
     float acc[8][4];
 #pragma unroll
     for (int n = 0; n < 8; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
-#pragma unroll
+#pragma unroll 2
     for (int k = 0; k < 8; ++k) {
-      uint32_t af[4];
-      gdn_ldsm_x4(smem_u32(sa + gdn_swz(wrow + (lane & 15), k * 2 + (lane >> 4))), af[0], af[1],
-                  af[2], af[3]);
+      uint32_t af[4], al[4];
+      const uint32_t aoff = gdn_swz(wrow + (lane & 15), k * 2 + (lane >> 4));
+      gdn_ldsm_x4(smem_u32(sa + aoff), af[0], af[1], af[2], af[3]);
+      gdn_ldsm_x4(smem_u32(sal + aoff), al[0], al[1], al[2], al[3]);
 #pragma unroll
       for (int n = 0; n < 8; n += 2) {
         const int i = lane >> 3;
         const int r = n * 8 + (i >> 1) * 8 + (lane & 7);
-        uint32_t b0, b1, b2, b3;
-        gdn_ldsm_x4(smem_u32(sk + gdn_swz(r, k * 2 + (i & 1))), b0, b1, b2, b3);
+        const uint32_t boff = gdn_swz(r, k * 2 + (i & 1));
+        uint32_t b0, b1, b2, b3, l0, l1, l2, l3;
+        gdn_ldsm_x4(smem_u32(sk + boff), b0, b1, b2, b3);
+        gdn_ldsm_x4(smem_u32(skl + boff), l0, l1, l2, l3);
         gdn_mma(acc[n], af, b0, b1);
         gdn_mma(acc[n + 1], af, b2, b3);
+        gdn_mma(acc[n], af, l0, l1);
+        gdn_mma(acc[n + 1], af, l2, l3);
+        gdn_mma(acc[n], al, b0, b1);
+        gdn_mma(acc[n + 1], al, b2, b3);
       }
     }
 #pragma unroll
@@ -442,9 +462,10 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(const GatedDeltaPar
     float r = 0.f;
     if (t < L) {
       if (isw) {
-        const __nv_bfloat16* kp = reinterpret_cast<const __nv_bfloat16*>(
-            sk + gdn_swz(t, j >> 3) + (j & 7) * 2);
-        r = sbeta[t] * __expf(slg[t]) * __bfloat162float(*kp);
+        const uint32_t off = gdn_swz(t, j >> 3) + (j & 7) * 2;
+        const float kv = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(sk + off)) +
+                         __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(skl + off));
+        r = sbeta[t] * __expf(slg[t]) * kv;
       } else {
         r = sbeta[t] * __bfloat162float(vcol[(long long)t * p.ld_qkv]);
       }
@@ -471,6 +492,8 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(const GatedDeltaPar
 // grid (B, Hv, 4), 256 threads: 32 value columns of one (sequence, value head), all chunks
 // of the sequence in order, the chunk products on the tensor cores (mma m16n8k8 tf32, fp32
 // accumulation; the state itself stays fp32 in shared memory).  Per chunk, 8 warps:
+// The two products that feed the carried state (W S0 and K^T (f Delta)) use 3xTF32 (operands
+// split into a tf32 pair), close to fp32; the two output products use single tf32.
 //   Delta[64 x 32] = U - W S0                 warp (m tile w % 4, 16 columns w / 4), k = 128
 //   O[64 x 32]     = qf * (Q S0) + QKm Delta  same tiling, k = 128 and k = 64 (lower blocks)
 //   S[128 x 32]    = gamma_L S0 + K^T (f * Delta)   warp = 16 state rows x 32 columns, k = 64
@@ -496,6 +519,11 @@ __device__ __forceinline__ void mma_tf32(float (&d)[4], uint32_t a0, uint32_t a1
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 __device__ __forceinline__ float bf(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+// x = big + small, both tf32 (3xTF32: big*big + big*small + small*big is close to fp32)
+__device__ __forceinline__ void tf32_split(float x, uint32_t& big, uint32_t& small) {
+  big = tf32(x);
+  small = tf32(x - __uint_as_float(big));
+}
 }  // namespace
 
 __global__ void __launch_bounds__(256) gdn_chunk_state_kernel(const GatedDeltaParams p,
@@ -574,15 +602,23 @@ __global__ void __launch_bounds__(256) gdn_chunk_state_kernel(const GatedDeltaPa
       float acc[2][4];
 #pragma unroll
       for (int j = 0; j < 2; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-#pragma unroll 4
+#pragma unroll 2
       for (int ks = 0; ks < 16; ++ks) {
         const int kc = ks * 8 + t4;
-        const uint32_t a0 = tf32(sW[r0 * kWStride + kc]), a1 = tf32(sW[r1 * kWStride + kc]);
-        const uint32_t a2 = tf32(sW[r0 * kWStride + kc + 4]), a3 = tf32(sW[r1 * kWStride + kc + 4]);
+        uint32_t a0, a1, a2, a3, e0, e1, e2, e3;
+        tf32_split(sW[r0 * kWStride + kc], a0, e0);
+        tf32_split(sW[r1 * kWStride + kc], a1, e1);
+        tf32_split(sW[r0 * kWStride + kc + 4], a2, e2);
+        tf32_split(sW[r1 * kWStride + kc + 4], a3, e3);
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
           const int col = nh * 16 + j * 8 + g;
-          mma_tf32(acc[j], a0, a1, a2, a3, tf32(sS[kc * kSS + col]), tf32(sS[(kc + 4) * kSS + col]));
+          uint32_t b0, b1, f0, f1;
+          tf32_split(sS[kc * kSS + col], b0, f0);
+          tf32_split(sS[(kc + 4) * kSS + col], b1, f1);
+          mma_tf32(acc[j], e0, e1, e2, e3, b0, b1);
+          mma_tf32(acc[j], a0, a1, a2, a3, f0, f1);
+          mma_tf32(acc[j], a0, a1, a2, a3, b0, b1);
         }
       }
 #pragma unroll
@@ -660,7 +696,12 @@ __global__ void __launch_bounds__(256) gdn_chunk_state_kernel(const GatedDeltaPa
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const int col = j * 8 + g;
-          mma_tf32(acc[j], a0, a1, a2, a3, tf32(fa * sD[kt * kSS + col]), tf32(fb * sD[(kt + 4) * kSS + col]));
+          // k is bf16, exact in tf32: splitting the (f * Delta) operand suffices
+          uint32_t b0, b1, f0, f1;
+          tf32_split(fa * sD[kt * kSS + col], b0, f0);
+          tf32_split(fb * sD[(kt + 4) * kSS + col], b1, f1);
+          mma_tf32(acc[j], a0, a1, a2, a3, f0, f1);
+          mma_tf32(acc[j], a0, a1, a2, a3, b0, b1);
         }
       }
 #pragma unroll

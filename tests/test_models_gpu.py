@@ -77,6 +77,27 @@ def test_hybrid_gpu_matches_cpu(cuda_device):
     _agree(_hybrid_ckpt(), tol=0.25)
 
 
+def test_hybrid_chunked_prefill_matches_recurrent(cuda_device):
+    """The same bf16 hybrid model with its DeltaNet prefill forced to the chunked kernels and to
+    the token recurrence: prefill logits of 150-token prompts (three chunks) agree."""
+    from vllm_neuron_b200.models.qwen3_5 import Qwen3_5MoeForCausalLM
+
+    d = _hybrid_ckpt()
+    prompts = random_prompts(n=3, length=150, vocab=1024)
+    got = {}
+    for mode in ("recurrent", "chunked"):
+        Qwen3_5MoeForCausalLM.deltanet_mode = mode
+        try:
+            llm = LLM(d, device="cuda:0", max_num_seqs=4, max_model_len=512, num_gpu_blocks=64,
+                      max_num_batched_tokens=512)
+            got[mode] = llm.engine.prompt_logits(prompts)
+        finally:
+            Qwen3_5MoeForCausalLM.deltanet_mode = "auto"
+    rel = ((got["chunked"] - got["recurrent"]).norm() / got["recurrent"].norm()).item()
+    assert rel < 0.1, rel
+    assert ext().read_status() == 0
+
+
 def test_qwen3_moe_gpu_matches_cpu(cuda_device):
     from transformers import Qwen3MoeConfig, Qwen3MoeForCausalLM
 

@@ -59,6 +59,7 @@ class ForwardBatch:
     positions3: torch.Tensor | None = None   # [T, 3] int32 M-RoPE positions (vision-language)
     deep_rows: torch.Tensor | None = None    # [n] int64 rows receiving DeepStack features
     deep_feats: torch.Tensor | None = None   # [n_deep, n, H] added after decoder layers 0..n_deep-1
+    max_q_len: int = 0                       # longest query of the step (host value; 0 = unknown)
 
 
 def _shard(n: int, world: int, rank: int) -> tuple[int, int]:

@@ -42,6 +42,10 @@ def num_state_slots(max_seqs: int) -> int:
 class Qwen3_5MoeForCausalLM(Qwen3MoeForCausalLM):
     supports_prefix_caching = False
 
+    # "auto" (chunked WY form for steps with a full 64-token chunk, else token by token),
+    # "chunked" or "recurrent"
+    deltanet_mode = "auto"
+
     def __init__(self, cfg, *args, **kw):
         tp = kw.get("tp")
         W = tp.world if tp is not None else 1
@@ -133,7 +137,8 @@ class Qwen3_5MoeForCausalLM(Qwen3MoeForCausalLM):
                 aa = proj[:, cd + Vd + Hv:cd + Vd + 2 * Hv]
                 core = DN.gated_delta_rule(conv, z, aa, bb, ly.A_log, ly.dt_bias, ly.gnorm_w, self.eps,
                                            b.q_start, b.seq_lens, slots, self.ssm_state[li],
-                                           self.ws_lin_out[:T], self.lin_Hk, self.lin_Hv)
+                                           self.ws_lin_out[:T], self.lin_Hk, self.lin_Hv,
+                                           mode=DN.pick_mode(T, b.max_q_len, self.deltanet_mode))
                 _linear(core, ly.out_proj, h)
             else:
                 k_cache, v_cache = self.kv_caches[self.kv_index[i]]

@@ -60,6 +60,15 @@ def gated_delta_rule(qkv: torch.Tensor, z: torch.Tensor, a: torch.Tensor, b: tor
     return out
 
 
+def pick_mode(T: int, max_q_len: int, mode: str = "auto") -> str:
+    """The kernel choice for a step: the chunked form once some sequence fills a 64-token
+    chunk (and the step has >= 128 tokens), the token recurrence otherwise; ``max_q_len``
+    0 (unknown) leaves the choice to the op."""
+    if mode != "auto" or max_q_len <= 0:
+        return mode
+    return "chunked" if (max_q_len >= 64 and T >= 128) else "recurrent"
+
+
 def gated_delta_rule_ref(qkv, z, a, b, A_log, dt_bias, norm_w, eps, q_start, seq_lens, slots,
                          state, Hk, Hv):
     dk, dv = state.shape[2], state.shape[3]

@@ -257,6 +257,7 @@ class ModelRunner:
         work = h[o["work"][0]:o["work"][0] + 2 * len(w.work)]
         work[:] = w.work.reshape(-1)
         self._last_work_len = len(w.work)
+        self._last_max_q = int(q_lens[:Bp].max()) if Bp and pad_B is None else 1
         return s, w.decode, w.num_splits
 
     def _attach_prompt_embeds(self, out: SchedulerOutput, fb: ForwardBatch):
@@ -348,6 +349,7 @@ class ModelRunner:
             q_start=sec("qstart", B + 1), work=sec("work", 2 * W).view(W, 2),
             logits_indices=sec("lidx", S),
             decode=decode, num_splits=splits, num_tokens=lay.T)
+        fb.max_q_len = 1 if decode else getattr(self, "_last_max_q", 0)
         fb.seq_slots = sec("sslot", B)
         samp = dict(temperature=sec("temp", S, torch.float32), top_k=sec("topk", S),
                     top_p=sec("topp", S, torch.float32), min_p=sec("minp", S, torch.float32),
