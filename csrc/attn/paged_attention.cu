@@ -453,6 +453,48 @@ __global__ void attn_combine_kernel(const float* __restrict__ part_o,
   }
 }
 
+// Same merge, one warp per (token, head) for up to 32 splits: lane s holds split s's
+// log-sum-exp, the weights come from two warp reductions, and each lane accumulates D / 32
+// contiguous dims of every split with vector loads.
+template <int D>
+__global__ void __launch_bounds__(256) attn_combine_warp_kernel(
+    const float* __restrict__ part_o, const float* __restrict__ part_lse, __nv_bfloat16* out,
+    long long o_stride_t, int total_tokens, int Hq, int num_splits) {
+  pdl_trigger();
+  pdl_wait();
+  constexpr int PER = D / 32;
+  const int wid = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (wid >= total_tokens * Hq) return;
+  const int tok = wid / Hq, head = wid - tok * Hq;
+  const long long row = (long long)tok * Hq + head;
+  const long long split_stride = (long long)total_tokens * Hq;
+  const float my = lane < num_splits ? part_lse[lane * split_stride + row] : -INFINITY;
+  const float mx = warp_max(my);
+  const float mu = mx == -INFINITY ? 0.f : mx;
+  const float wl = lane < num_splits ? exp2f(my - mu) : 0.f;
+  const float den = warp_sum(wl);
+  const float inv = den > 0.f ? 1.f / den : 0.f;
+  float acc[PER];
+#pragma unroll
+  for (int e = 0; e < PER; ++e) acc[e] = 0.f;
+  for (int sp = 0; sp < num_splits; ++sp) {
+    const float wgt = __shfl_sync(0xffffffffu, wl, sp);
+    if (wgt == 0.f) continue;  // empty split (uniform over the warp)
+    const float* src = part_o + (sp * split_stride + row) * D + lane * PER;
+#pragma unroll
+    for (int e = 0; e < PER; e += 2) {
+      const float2 v = *reinterpret_cast<const float2*>(src + e);
+      acc[e] += wgt * v.x;
+      acc[e + 1] += wgt * v.y;
+    }
+  }
+  __nv_bfloat16* dst = out + (long long)tok * o_stride_t + (long long)head * D + lane * PER;
+#pragma unroll
+  for (int e = 0; e < PER; e += 2)
+    *reinterpret_cast<uint32_t*>(dst + e) = pack_bf16x2(acc[e] * inv, acc[e + 1] * inv);
+}
+
 template <int D, bool DECODE, bool FP8>
 static void launch_attn_t(const PagedAttnParams& p, int num_work, cudaStream_t stream) {
   constexpr int BM = DECODE ? 16 : 64;
@@ -491,7 +533,20 @@ void paged_attention_launch(const PagedAttnParams& p, int num_work, int head_dim
     throw std::invalid_argument("paged_attention: unsupported head_dim " +
                                 std::to_string(head_dim));
   }
-  if (p.num_splits > 1) {
+  if (p.num_splits > 1 && p.num_splits <= 32) {
+    const dim3 grid((unsigned)((p.total_tokens * p.Hq + 7) / 8));
+    const float* po = p.part_o;
+    const float* pl = p.part_lse;
+    if (head_dim == 128)
+      launch_pdl(attn_combine_warp_kernel<128>, grid, dim3(256), 0, stream, po, pl, p.out,
+                 p.o_stride_t, p.total_tokens, p.Hq, p.num_splits);
+    else if (head_dim == 256)
+      launch_pdl(attn_combine_warp_kernel<256>, grid, dim3(256), 0, stream, po, pl, p.out,
+                 p.o_stride_t, p.total_tokens, p.Hq, p.num_splits);
+    else
+      launch_pdl(attn_combine_warp_kernel<64>, grid, dim3(256), 0, stream, po, pl, p.out,
+                 p.o_stride_t, p.total_tokens, p.Hq, p.num_splits);
+  } else if (p.num_splits > 1) {
     dim3 grid(p.total_tokens, p.Hq);
     if (head_dim == 128)
       launch_pdl(attn_combine_kernel<128>, grid, dim3(128), 0, stream, (const float*)p.part_o,

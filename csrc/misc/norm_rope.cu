@@ -189,7 +189,7 @@ void add_rmsnorm_launch(void* x, bool x_is_f32, long long x_stride, __nv_bfloat1
 }
 
 // ------------------------------------------------------------------------------------------
-// RoPE + optional q/k RMSNorm + paged KV write.  One CTA per token, one warp per head.
+// RoPE + optional q/k RMSNorm + paged KV write.  One warp per (token, head); 8 heads per CTA.
 // Input row layout: [q heads | k heads | v heads] * D.  The rotated q is written to q_out
 // (bf16, may alias the input when the input is bf16).
 // ------------------------------------------------------------------------------------------
@@ -206,7 +206,11 @@ __global__ void __launch_bounds__(256) rope_kv_write_kernel(const RopeKvParams p
   const float* cs = p.cos_sin + (long long)pos * p.rot_dim;  // [cos(half) | sin(half)]
   const int nheads = p.Hq + 2 * p.Hkv;
   TIN* row = qkv + (long long)t * p.qkv_stride;
-  for (int h = warp; h < nheads; h += blockDim.x >> 5) {
+  // blockIdx.y selects a group of heads (one per warp), so small decode batches still fill
+  // the SMs
+  const int wpc = blockDim.x >> 5;
+  const int h_end = min(nheads, ((int)blockIdx.y + 1) * wpc);
+  for (int h = (int)blockIdx.y * wpc + warp; h < h_end; h += wpc) {
     const bool is_q = h < p.Hq;
     const bool is_k = !is_q && h < p.Hq + p.Hkv;
     TIN* src = row + (long long)h * D;
@@ -314,13 +318,15 @@ void rope_kv_write_launch(const RopeKvParams& p, void* qkv, bool qkv_is_f32, int
   if (T == 0) return;
   if (p.positions3 != nullptr && !(p.neox && p.rot_dim == p.head_dim && p.head_dim >= 64))
     throw std::invalid_argument("rope_kv_write: multimodal RoPE needs full-width neox rotation");
+  // one warp per head: 8 heads per CTA, grid (tokens, head groups)
+  const dim3 grid(T, (p.Hq + 2 * p.Hkv + 7) / 8);
 #define B200_ROPE(D_)                                                                       \
   if (p.head_dim == D_) {                                                                   \
     if (qkv_is_f32)                                                                         \
-      launch_pdl(rope_kv_write_kernel<float, D_>, dim3(T), dim3(256), 0, stream, p,          \
+      launch_pdl(rope_kv_write_kernel<float, D_>, grid, dim3(256), 0, stream, p,             \
                  (float*)qkv);                                                              \
     else                                                                                    \
-      launch_pdl(rope_kv_write_kernel<__nv_bfloat16, D_>, dim3(T), dim3(256), 0, stream, p,  \
+      launch_pdl(rope_kv_write_kernel<__nv_bfloat16, D_>, grid, dim3(256), 0, stream, p,     \
                  (__nv_bfloat16*)qkv);                                                      \
     return;                                                                                 \
   }
