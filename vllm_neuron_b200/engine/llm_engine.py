@@ -473,6 +473,34 @@ class LLMEngine:
             done.extend(self.step())
         return done
 
+    def run_lockstep(self, group) -> list[Request]:
+        """Serve this replica's requests in lockstep with the other data-parallel replicas of
+        ``group`` (gloo): every iteration all replicas agree (MAX all-reduce of two flags) on
+        whether any of them has a batch; a replica with nothing scheduled then runs a one-token
+        dummy forward so that the collectives inside the model (all-to-all expert exchange)
+        match.  Synchronous scheduling only.  Reference: the DP padding all-reduce and dummy
+        batch (vllm_neuron/vllm/worker/neuron_model_runner.py:7337-7489, 7710)."""
+        import torch.distributed as dist
+
+        done = []
+        while True:
+            out = self.scheduler.schedule()
+            flags = torch.tensor([0 if out.empty else 1, 1 if self.scheduler.has_unfinished() else 0],
+                                 dtype=torch.int64)
+            dist.all_reduce(flags, op=dist.ReduceOp.MAX, group=group)
+            if flags[0] == 0:
+                if flags[1] == 0:
+                    return done
+                continue
+            if out.empty:
+                self.runner.dummy_forward()
+                continue
+            want_lp = any(s.req.sampling_params.logprobs for s in out.scheduled if s.samples)
+            handle = self.runner.launch(out, want_logprobs=want_lp)
+            self.num_steps += 1
+            self.metrics.steps += 1
+            done.extend(self._process(out, handle))
+
     @staticmethod
     def to_output(req: Request) -> RequestOutput:
         reason = {RequestStatus.FINISHED_STOPPED: "stop", RequestStatus.FINISHED_LENGTH: "length",

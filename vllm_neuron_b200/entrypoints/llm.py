@@ -52,7 +52,7 @@ class LLM:
                  enforce_eager: bool = False, device: str | None = None, dtype: str = "auto",
                  async_scheduling: bool | None = None, speculative_config: dict | None = None,
                  data_parallel_size: int | None = None, mm_processor_kwargs: dict | None = None,
-                 kv_cache_dtype: str = "auto", **unused):
+                 kv_cache_dtype: str = "auto", enable_expert_parallel: bool = False, **unused):
         if device is None:
             device = f"cuda:{torch.cuda.current_device()}" if torch.cuda.is_available() else "cpu"
         ps.init_distributed(backend="gloo" if str(device).startswith("cpu") else None)
@@ -72,6 +72,11 @@ class LLM:
         self.dp_size = dp
         self.dp_rank = (torch.distributed.get_rank() // tensor_parallel_size) if world > 1 else 0
         self._dp_group = st.dp_cpu
+        # Wide expert parallelism: with data-parallel replicas, an all-to-all backend and
+        # enable_expert_parallel, MoE experts are sharded over every rank and tokens move by
+        # all-to-all (reference: all2all_backend, vllm_neuron/parallel/all2all.py:33-641).
+        nc = (additional_config or {}).get("neuron_config") or (additional_config or {}).get("b200_config") or {}
+        st.ep_all2all = bool(dp > 1 and enable_expert_parallel and nc.get("all2all_backend"))
         if dtype == "auto":
             dtype = "bfloat16" if str(device).startswith("cuda") else "float32"
         args = EngineArgs(model=model, max_num_seqs=max_num_seqs,
@@ -110,7 +115,13 @@ class LLM:
 
     def _generate_dp(self, prompts, sampling_params) -> list[RequestOutput]:
         mine = [i for i in range(len(prompts)) if i % self.dp_size == self.dp_rank]
-        local = self._generate([prompts[i] for i in mine], [sampling_params[i] for i in mine]) if mine else []
+        if getattr(self.engine.model, "a2a", None) is not None:
+            # replicas share the MoE layers' all-to-alls: step in lockstep, idle ones run a
+            # one-token dummy forward (reference: DP dummy batch, neuron_model_runner.py:7710)
+            local = self._generate([prompts[i] for i in mine], [sampling_params[i] for i in mine],
+                                   lockstep=self._dp_group)
+        else:
+            local = self._generate([prompts[i] for i in mine], [sampling_params[i] for i in mine]) if mine else []
         parts = [None] * self.dp_size
         torch.distributed.all_gather_object(parts, (mine, local), group=self._dp_group)
         res = [None] * len(prompts)
@@ -119,7 +130,7 @@ class LLM:
                 res[i] = o
         return res
 
-    def _generate(self, prompts, sampling_params) -> list[RequestOutput]:
+    def _generate(self, prompts, sampling_params, lockstep=None) -> list[RequestOutput]:
         ids = []
         base = self.engine.num_steps * 1_000_003
         for i, (p, sp) in enumerate(zip(prompts, sampling_params)):
@@ -139,7 +150,8 @@ class LLM:
                 continue
             toks = _normalize_prompt(p, self.tokenizer)
             ids.append(self.engine.add_request(toks, sp, request_id=f"gen-{base}-{i}"))
-        done = {r.request_id: r for r in self.engine.run_until_done()}
+        done = {r.request_id: r for r in (self.engine.run_lockstep(lockstep) if lockstep is not None
+                                          else self.engine.run_until_done())}
         outs = []
         for rid in ids:
             o = LLMEngine.to_output(done[rid])

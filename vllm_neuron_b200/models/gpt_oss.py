@@ -21,6 +21,7 @@ import torch
 from .. import envs, ops
 from ..ops import moe as M
 from .llama import LlamaForCausalLM
+from .qwen_moe import MoEMixin
 
 # e2m1 code points (sign bit 3, exponent bits 2-1, mantissa bit 0)
 _FP4_VALUES = [0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0, -0.0, -0.5, -1.0, -1.5, -2.0, -3.0, -4.0, -6.0]
@@ -65,16 +66,19 @@ def _quant_experts(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     return torch.stack(bl), torch.stack(sc)
 
 
-class GptOssForCausalLM(LlamaForCausalLM):
+class GptOssForCausalLM(MoEMixin, LlamaForCausalLM):
+    route_mode = M.ROUTE_TOPK_SOFTMAX
+    expert_act = M.ACT_GPTOSS
+    renorm = True
+
     def __init__(self, cfg, *args, **kw):
         W = kw.get("tp").world if kw.get("tp") is not None else 1
         self.E = cfg.num_experts
         self.topk = cfg.num_experts_per_tok
-        assert self.E % W == 0, f"{self.E} experts not divisible by TP={W}"
-        self.e_local = self.E // W
+        self._shard_experts(W)  # by index over TP, or over the EP group with all-to-all
         self.I_moe = cfg.intermediate_size
         super().__init__(cfg, *args, **kw)
-        self.e_start = self.tp.rank * self.e_local
+        self.e_start = self.a2a.e_start if self.a2a is not None else self.tp.rank * self.e_local
         p = lambda *s: torch.nn.Parameter(torch.empty(*s, dtype=self.dtype, device=self.device),
                                           requires_grad=False)
         for ly in self.layers:
@@ -118,6 +122,11 @@ class GptOssForCausalLM(LlamaForCausalLM):
 
     def _mlp(self, i, ly, x, res, nxt_norm, T, small, fused):
         h = self.ws_h[:T]
+        if self.a2a is not None:
+            self._moe_all2all(ly, x[:T], h, b_gu=ly.b_gu, b_down=ly.b_down, alpha=self.cfg.swiglu_alpha,
+                              limit=self.cfg.swiglu_limit)
+            self._reduce_norm(h, res, nxt_norm, x)
+            return
         M.moe_block(x, ly.router, ly.w_gu, ly.w_down, self.topk, M.ROUTE_TOPK_SOFTMAX,
                     router_b=ly.router_bias, b_gu=ly.b_gu,
                     b_down=ly.b_down,  # each assignment is computed on exactly one rank

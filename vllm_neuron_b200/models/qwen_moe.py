@@ -34,14 +34,34 @@ class MoEMixin:
         W = tp.world if tp is not None else 1
         self.E = cfg.num_experts
         self.topk = cfg.num_experts_per_tok
-        assert self.E % W == 0, f"{self.E} experts not divisible by TP={W}"
-        self.e_local = self.E // W
+        self._shard_experts(W)
         self.I_moe = cfg.moe_intermediate_size or cfg.intermediate_size
         self.I_sh = (cfg.shared_expert_intermediate_size or 0) // W
         self.renorm = bool(cfg.norm_topk_prob)
 
+    def _shard_experts(self, W: int):
+        """Experts by index over the TP group (partials summed by the all-reduce), or over the
+        EP group with all-to-all token exchange when wide EP is configured."""
+        from ..parallel import state as ps
+
+        self.a2a = None
+        st = ps.get_parallel_state()
+        if getattr(st, "ep_all2all", False) and st.ep.world > 1:
+            # wide EP: experts sharded over the EP group, whose ranks hold different tokens
+            # (data-parallel replicas); tokens travel by all-to-all (parallel/all2all.py)
+            if W > 1:
+                raise NotImplementedError("all-to-all expert parallelism needs TP=1 per data-parallel replica")
+            from ..parallel.all2all import All2AllManager
+
+            self.a2a = All2AllManager(st.ep.group, st.ep.rank, st.ep.world, self.E)
+            self.e_local = self.a2a.e_local
+            self.supports_cuda_graphs = False  # host-side split sizes per exchange
+        else:
+            assert self.E % W == 0, f"{self.E} experts not divisible by TP={W}"
+            self.e_local = self.E // W
+
     def _post_init_moe(self):
-        self.e_start = self.tp.rank * self.e_local
+        self.e_start = self.a2a.e_start if self.a2a is not None else self.tp.rank * self.e_local
         self.moe_ws = None
         if self.device.type == "cuda":
             self.moe_ws = M.MoEWorkspace.create(self.max_tokens + self.tp.world, self.topk, self.E, self.e_local, self.H,
@@ -59,12 +79,49 @@ class MoEMixin:
 
     def _moe_mlp(self, ly, x, res, nxt_norm, T):
         h = self.ws_h[:T]
-        M.moe_block(x, ly.router, ly.w_gu, ly.w_down, self.topk, self.route_mode, self.renorm,
-                    router_b=getattr(ly, "router_bias", None), act=self.expert_act,
-                    e_start=self.e_start, ws=self.moe_ws, out=h, num_experts=self.E,
-                    shared_gu=ly.sh_gu, shared_down=ly.sh_down, routed_scale=self.routed_scale,
-                    shared_gated=self.shared_gated)
+        if self.a2a is not None:
+            self._moe_all2all(ly, x[:T], h)
+        else:
+            M.moe_block(x, ly.router, ly.w_gu, ly.w_down, self.topk, self.route_mode, self.renorm,
+                        router_b=getattr(ly, "router_bias", None), act=self.expert_act,
+                        e_start=self.e_start, ws=self.moe_ws, out=h, num_experts=self.E,
+                        shared_gu=ly.sh_gu, shared_down=ly.sh_down, routed_scale=self.routed_scale,
+                        shared_gated=self.shared_gated)
         self._reduce_norm(h, res, nxt_norm, x)
+
+    def _moe_all2all(self, ly, x, out, b_gu=None, b_down=None, alpha=1.702, limit=7.0):
+        """Route the local tokens, dispatch them to the ranks owning their experts, run this
+        rank's experts on the rows received, send the pre-reduced rows back and sum them per
+        token; the shared expert (replicated) runs on the local tokens.  Reference:
+        vllm_neuron/parallel/all2all.py:33-641 with functional/moe/moe_tkg.py:17 on the A2A-v
+        input layout."""
+        from ..ops import ep as EP
+        from ..ops import linear as L
+
+        E = self.E
+        if x.is_cuda:
+            logits = L.gemm_out(x, ly.router)
+        else:
+            logits = (x.float() @ ly.router.float().t()).to(x.dtype)
+        sh_gu = getattr(ly, "sh_gu", None)
+        gated = sh_gu is not None and self.shared_gated
+        ids, w = M.route(logits, self.topk, self.route_mode, self.renorm, getattr(ly, "router_bias", None),
+                         num_experts=E, scale=self.routed_scale)
+        plan, rows, aff = self.a2a.dispatch(x, ids, w)
+        lids, lw = EP.local_routing(aff, self.e_start, self.topk)
+        part = M.moe_experts(rows, lids, lw, ly.w_gu, ly.w_down, b_gu, b_down, self.expert_act, alpha,
+                             limit, e_start=self.e_start)
+        y = self.a2a.combine(part, plan).float()
+        if sh_gu is not None:
+            if x.is_cuda:
+                from ..ops.activation import silu_mul
+
+                sh = L.gemm_out(silu_mul(L.gemm_out(x, ly.sh_gu)), ly.sh_down).float()
+            else:
+                sh = M.shared_expert_ref(x, ly.sh_gu, ly.sh_down)
+            gate = torch.sigmoid(logits[:, E:E + 1].float()) if gated else 1.0
+            y = y + gate * sh
+        out.copy_(y.to(out.dtype))
 
 
 class Qwen3MoeForCausalLM(MoEMixin, LlamaForCausalLM):

@@ -271,6 +271,38 @@ def moe_block(x: torch.Tensor, router_w: torch.Tensor, w_gu: torch.Tensor, w_dow
         gu_sh = L.gemm_out(x, shared_gu, out=ws.shared_gu[:T])
         a_sh = silu_mul(gu_sh, out=ws.shared_act[:T])
         shared = L.gemm_out(a_sh, shared_down, out=ws.shared[:T])
+    return _experts_cuda(x, ids, w, w_gu, w_down, k, b_gu, b_down, act, alpha, limit, e_start, ws,
+                         out, shared, ws.shared_gate[:T] if gated else None, fp4_gu, fp4_down,
+                         fp4_max_tokens)
+
+
+def moe_experts(x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, w_gu: torch.Tensor,
+                w_down: torch.Tensor, b_gu: torch.Tensor | None = None,
+                b_down: torch.Tensor | None = None, act: int = ACT_SILU, alpha: float = 1.702,
+                limit: float = 7.0, e_start: int = 0, out: torch.Tensor | None = None) -> torch.Tensor:
+    """The expert half of :func:`moe_block` for given routing ``ids, w [R, k]`` (ids outside
+    ``[e_start, e_start + e_local)`` contribute nothing): ``out[r] = sum_j w[r, j] *
+    expert_{ids[r, j]}(x[r])`` in bf16.  Used on the rows an expert-parallel dispatch delivered."""
+    R, H = x.shape
+    k = ids.shape[1]
+    if out is None:
+        out = torch.empty(R, H, dtype=x.dtype if not x.is_cuda else torch.bfloat16, device=x.device)
+    if not x.is_cuda:
+        out.copy_(experts_ref(x, ids, w, w_gu, w_down, b_gu, b_down, act, alpha, limit, e_start).to(out.dtype))
+        return out
+    if R == 0:
+        return out
+    e_local, I2, _ = w_gu.shape
+    ws = MoEWorkspace.create(R, k, e_start + e_local, e_local, H, I2 // 2, x.device)
+    return _experts_cuda(x, ids.to(torch.int32).contiguous(), w.float().contiguous(), w_gu, w_down, k,
+                         b_gu, b_down, act, alpha, limit, e_start, ws, out, None, None, None, None, 0)
+
+
+def _experts_cuda(x, ids, w, w_gu, w_down, k, b_gu, b_down, act, alpha, limit, e_start, ws, out,
+                  shared, shared_gate, fp4_gu, fp4_down, fp4_max_tokens):
+    T, H = x.shape
+    e_local, I2, _ = w_gu.shape
+    I = I2 // 2
     R = T * k
     ext().moe_align(ids, e_start, e_local, ws.offsets, ws.sorted_src, ws.row_expert,
                     ws.inv_pos[:R], ws.gtiles, ws.gcount)
@@ -291,6 +323,5 @@ def moe_block(x: torch.Tensor, router_w: torch.Tensor, w_gu: torch.Tensor, w_dow
         ext().moe_mxfp4_gemm(a, fp4_down, y, gt, ws.gcount)
     else:
         ext().gemm_grouped(a, w_down, y, ws.gtiles, ws.gcount, EPI_BF16, 256 if H % 256 == 0 else 128)
-    ext().moe_combine(y, ws.inv_pos[:R], w, ids, b_down, e_start, shared,
-                      ws.shared_gate[:T] if gated else None, out)
+    ext().moe_combine(y, ws.inv_pos[:R], w, ids, b_down, e_start, shared, shared_gate, out)
     return out

@@ -101,6 +101,9 @@ class ParallelState:
     cpu: dist.ProcessGroup | None = None
     dp_cpu: dist.ProcessGroup | None = None   # gloo group of this rank's DP peers
     groups: dict = field(default_factory=dict)
+    # MoE experts sharded over the EP group with all-to-all token exchange (wide EP across
+    # data-parallel replicas); replicas then step in lockstep
+    ep_all2all: bool = False
 
 
 _STATE: ParallelState | None = None

@@ -411,6 +411,33 @@ class ModelRunner:
             torch.cuda.synchronize(self.device)
             self.graphs[b] = (g, lay, buf, tok, lp, w.num_splits)
 
+    def dummy_forward(self):
+        """A one-token forward on the null block that writes no KV and samples nothing: an idle
+        data-parallel replica runs it so the collectives inside the model (the MoE all-to-alls
+        of wide expert parallelism) stay matched across replicas (reference: the DP dummy batch,
+        vllm_neuron/vllm/worker/neuron_model_runner.py:7710)."""
+        m = self.model
+        lay = Layout(1, 1, 1, 1, self.max_blocks)
+        G = max(1, m.Hq // m.Hkv)
+        w = ops.build_work(np.ones(1, dtype=np.int64), np.ones(1, dtype=np.int64), G, m.Hkv,
+                           self.num_sms, max_splits=1, head_dim=m.D)
+        h = torch.zeros(lay.total, dtype=torch.int32)
+        o = lay.off
+        h[o["qstart"][0]:o["qstart"][0] + 2] = torch.arange(2, dtype=torch.int32)
+        h[o["seqlen"][0]] = 1
+        h[o["slot"][0]] = -1
+        h[o["work"][0]:o["work"][0] + 2 * len(w.work)] = torch.from_numpy(w.work.reshape(-1))
+        h[o["topp"][0]] = torch.tensor([1.0]).view(torch.int32)
+        h[o["rslot"][0]] = self.pad_slot
+        h[o["sslot"][0]] = self.pad_slot
+        buf = self.dev_buf[:lay.total]
+        buf.copy_(h)
+        fb, _ = self._views(buf, lay, 1, 1, len(w.work), True, w.num_splits)
+        fb.work = fb.work[:len(w.work)]
+        self.model.forward(fb)
+        if self.is_cuda:
+            torch.cuda.synchronize(self.device)
+
     def release_graphs(self):
         self.graphs.clear()
 
