@@ -38,6 +38,7 @@ def main():
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--json", type=str, default=None)
     ap.add_argument("--no-fused", action="store_true", help="TP: NCCL all-reduce instead of the fused kernel")
+    ap.add_argument("--sp", action="store_true", help="TP prefill: sequence parallelism (fused unless --no-fused)")
     ap.add_argument("--emulate-tp", type=int, default=1,
                     help="one GPU runs rank 0's share of TP=N with local no-op collectives (profiling only)")
     ap.add_argument("--profile-once", action="store_true",
@@ -65,7 +66,8 @@ def main():
                                    num_gpu_blocks=blocks), tp=EmulatedRankComm(a.emulate_tp))
     else:
         llm = LLM(cfg, tensor_parallel_size=world,
-                  additional_config={"b200_config": {"fused_comm": not a.no_fused}},
+                  additional_config={"b200_config": {"fused_comm": not a.no_fused,
+                                                     "sequence_parallel": a.sp}},
                   max_num_seqs=B, max_model_len=max_len, max_num_batched_tokens=a.chunk,
                   load_format="dummy", num_gpu_blocks=blocks, skip_tokenizer_init=True)
         eng = llm.engine

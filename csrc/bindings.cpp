@@ -108,6 +108,94 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, int64_t epi
   check_launch("gemm");
 }
 
+static void fill_ptrs(const std::vector<int64_t>& v, void** dst, const char* what);
+
+// Sequence-parallel GEMM: optional all-gather wait on the A rows (ag_ctr != 0: local counter
+// array address, ag_targets per source rank, ag_rows rows per rank) and / or the reduce-scatter
+// epilogue (epi == EPI_BF16_RS: rs_out / rs_ctr peer addresses per owner rank, rs_rows rows per
+// owner; `out` is then only a shape / stride carrier).
+void gemm_sp(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, int64_t epi, int64_t bn,
+             int64_t ag_ctr, const std::vector<int64_t>& ag_targets, int64_t ag_rows,
+             const std::vector<int64_t>& rs_out, const std::vector<int64_t>& rs_ctr, int64_t rs_rows) {
+  CHECK_CUDA(a);
+  CHECK_CUDA(b);
+  CHECK_BF16(a);
+  CHECK_BF16(b);
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.size(1) == b.size(1), "gemm_sp: bad shapes");
+  TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1 && out.stride(-1) == 1,
+              "gemm_sp: inner dims must be contiguous");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16, "gemm_sp: bf16 output");
+  TORCH_CHECK(ag_targets.size() <= (size_t)b200::kGemmMaxRanks && rs_out.size() == rs_ctr.size() &&
+                  rs_out.size() <= (size_t)b200::kGemmMaxRanks, "gemm_sp: too many ranks");
+  const c10::cuda::CUDAGuard guard(a.device());
+  b200::GemmSPArgs sp{};
+  sp.ag_ctr = reinterpret_cast<const unsigned int*>(ag_ctr);
+  for (size_t r = 0; r < ag_targets.size(); ++r) sp.ag_target[r] = (unsigned int)ag_targets[r];
+  sp.ag_rows = (int)ag_rows;
+  sp.ag_world = (int)ag_targets.size();
+  for (size_t r = 0; r < rs_out.size(); ++r) {
+    sp.rs_out[r] = reinterpret_cast<__nv_bfloat16*>(rs_out[r]);
+    sp.rs_ctr[r] = reinterpret_cast<unsigned int*>(rs_ctr[r]);
+  }
+  sp.rs_rows = (int)rs_rows;
+  b200::GemmArgs g{};
+  g.A = a.data_ptr();
+  g.B = b.data_ptr();
+  g.out = out.data_ptr();
+  g.lda = a.stride(0);
+  g.ldb = b.stride(0);
+  g.ldo = out.stride(0);
+  g.M = (int)a.size(0);
+  g.N = (int)b.size(0);
+  g.K = (int)a.size(1);
+  g.bn = (int)bn;
+  g.epi = (int)epi;
+  g.splits = 1;
+  g.status = status_word();
+  g.sp = &sp;
+  if (g.M == 0 || g.N == 0) return;
+  b200::gemm_bf16_launch(g, cur_stream());
+  check_launch("gemm_sp");
+}
+
+void sp_norm_push(int64_t slots, int64_t slot_src_stride, int64_t nsrc, int64_t rs_ctr,
+                  int64_t rs_target, at::Tensor& residual, const at::Tensor& w, double eps,
+                  const std::vector<int64_t>& x_out, const std::vector<int64_t>& ag_ctr) {
+  CHECK_CUDA(residual);
+  CHECK_BF16(residual);
+  CHECK_BF16(w);
+  TORCH_CHECK(residual.is_contiguous(), "sp_norm_push: residual rows must be contiguous");
+  TORCH_CHECK(x_out.size() == ag_ctr.size() && !x_out.empty() && x_out.size() <= (size_t)b200::kMaxTP,
+              "sp_norm_push: rank lists");
+  const c10::cuda::CUDAGuard guard(residual.device());
+  b200::SPNormPushParams p{};
+  p.slots = reinterpret_cast<const __nv_bfloat16*>(slots);
+  p.slot_src_stride = slot_src_stride;
+  p.nsrc = (int)nsrc;
+  p.rs_ctr = reinterpret_cast<const unsigned int*>(rs_ctr);
+  p.rs_target = (unsigned int)rs_target;
+  p.residual = reinterpret_cast<__nv_bfloat16*>(residual.data_ptr());
+  p.w = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
+  p.eps = (float)eps;
+  fill_ptrs(x_out, (void**)p.x_out, "x_out");
+  fill_ptrs(ag_ctr, (void**)p.ag_ctr, "ag_ctr");
+  p.world = (int)x_out.size();
+  p.rows = (int)residual.size(0);
+  p.H = (int)residual.size(1);
+  p.status = status_word();
+  b200::sp_norm_push_launch(p, cur_stream());
+  check_launch("sp_norm_push", p.rows > 0 ? 1 : 0);
+}
+
+void sp_wait(int64_t ctr, const std::vector<int64_t>& targets) {
+  TORCH_CHECK(!targets.empty() && targets.size() <= (size_t)b200::kMaxTP, "sp_wait: targets");
+  unsigned int t[b200::kMaxTP] = {};
+  for (size_t r = 0; r < targets.size(); ++r) t[r] = (unsigned int)targets[r];
+  b200::sp_wait_launch(reinterpret_cast<const unsigned int*>(ctr), t, (int)targets.size(),
+                       status_word(), cur_stream());
+  check_launch("sp_wait");
+}
+
 void paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
                      const at::Tensor& block_tables, const at::Tensor& seq_lens,
                      const at::Tensor& q_start, const at::Tensor& work, at::Tensor& out,
@@ -703,6 +791,9 @@ int64_t launch_count() { return g_launches.load(); }
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels of vllm_neuron_b200";
   m.def("gemm", &gemm);
+  m.def("gemm_sp", &gemm_sp);
+  m.def("sp_norm_push", &sp_norm_push);
+  m.def("sp_wait", &sp_wait);
   m.def("paged_attention", &paged_attention);
   m.def("add_rmsnorm", &add_rmsnorm);
   m.def("rope_kv_write", &rope_kv_write);

@@ -36,6 +36,35 @@ struct TPArNormParams {
 };
 
 void tp_allreduce_norm_launch(const TPArNormParams& p, cudaStream_t stream);
+
+// Sequence-parallel prefill: the consumer of a reduce-scatter GEMM (EPI_BF16_RS) fused with the
+// residual add, RMSNorm and the all-gather push of the normalized rows (sp_fused.cu).  For each
+// of this rank's `rows` token rows: wait until every source's counter reaches rs_target, sum
+// the sources' bf16 partial rows in rank order, residual += sum, y = rmsnorm(residual) * w, store
+// y into every rank's all-gather buffer (x_out[r] + row * H, NVLink stores to peers) and finally
+// raise every rank's ag_ctr[r] (that rank's counter for this source) once per CTA.
+struct SPNormPushParams {
+  const __nv_bfloat16* slots;       // local receive slots of this call: [world][slot_rows][H]
+  long long slot_src_stride;        // elements between sources' slots
+  int nsrc;                         // 0: nothing to sum (first layer: residual already reduced)
+  const unsigned int* rs_ctr;       // local [world] counters raised by the sources' GEMMs
+  unsigned int rs_target;
+  __nv_bfloat16* residual;          // [rows][H], updated in place
+  const __nv_bfloat16* w;           // [H]
+  float eps;
+  __nv_bfloat16* x_out[kMaxTP];     // per rank: its all-gather buffer at this rank's first row
+  unsigned int* ag_ctr[kMaxTP];     // per rank: its counter for this source
+  int world, rows, H;
+  uint32_t* status;
+};
+void sp_norm_push_launch(const SPNormPushParams& p, cudaStream_t stream);
+struct SPWaitTargets {
+  unsigned int v[kMaxTP];
+};
+// Bounded wait until ctr[r] >= target[r] for r < world (one CTA); orders later kernels after
+// the peers' pushes.
+void sp_wait_launch(const unsigned int* ctr, const unsigned int* targets_host, int world,
+                    uint32_t* status, cudaStream_t stream);
 void flag_wait_probe_launch(const unsigned int* flag, unsigned int target, unsigned long long timeout_ns,
                             uint32_t* status, int* result, cudaStream_t stream);
 

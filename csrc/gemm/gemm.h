@@ -12,6 +12,27 @@ enum GemmEpilogue : int {
   EPI_F32_RED = 2,    // out[m, n] += D          (fp32 reduction, split-K)
   EPI_F32_RED_T = 3,  // out[n, m] += D          (fp32 reduction, swapped operands)
   EPI_SILU_BF16 = 4,  // out[m, j] = silu(gate) * up, gate/up interleaved per BN tile
+  EPI_BF16_RS = 5,    // row m -> rank m / rs_rows (bf16 peer store) + per-tile counters
+};
+
+constexpr int kGemmMaxRanks = 8;
+
+// Sequence-parallel fusion of a GEMM with the all-gather of its A rows and / or the
+// reduce-scatter of its output rows over NVLink peer memory.
+struct GemmSPArgs {
+  // A rows [r * ag_rows, (r + 1) * ag_rows) are pushed by rank r into this rank's A buffer;
+  // they are complete once ag_ctr[r] (this rank's memory, incremented by rank r) reaches
+  // ag_target[r].  The TMA producer waits per rank before loading those rows.
+  const unsigned int* ag_ctr = nullptr;
+  unsigned int ag_target[kGemmMaxRanks] = {};
+  int ag_rows = 0;
+  int ag_world = 0;
+  // EPI_BF16_RS: output row m is stored at rs_out[m / rs_rows] + (m % rs_rows) * ldo (rank
+  // m / rs_rows's receive slot for this rank), and after each tile rs_ctr[r] += 1 for every
+  // rank r whose rows the tile holds (release, system scope).
+  __nv_bfloat16* rs_out[kGemmMaxRanks] = {};
+  unsigned int* rs_ctr[kGemmMaxRanks] = {};
+  int rs_rows = 0;
 };
 
 struct GemmArgs {
@@ -32,6 +53,7 @@ struct GemmArgs {
   const int* gcount = nullptr;
   int gmax = 0;
   int num_groups = 0;
+  const GemmSPArgs* sp = nullptr;  // sequence-parallel fusion (null: plain GEMM)
 };
 
 void gemm_bf16_launch(const GemmArgs& args, cudaStream_t stream);

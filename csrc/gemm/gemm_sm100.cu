@@ -18,6 +18,13 @@
 //   EPI_F32_RED_T out[n, m] += D
 //   EPI_SILU_BF16 out[m, j] = silu(D[m, g]) * D[m, u] where the weight rows of each BN tile
 //                 are [BN/2 gate rows | BN/2 up rows] (interleaved at load time)
+//   EPI_BF16_RS   reduce-scatter epilogue of sequence parallelism: row m is stored (bf16) into
+//                 the receive slot of the rank that owns it, in that rank's memory over
+//                 NVLink, and each finished tile raises the owners' counters
+//
+// Sequence-parallel all-gather: with GemmSPArgs::ag_ctr set, the A rows of rank r are pushed
+// into this rank's A buffer by rank r; the producer waits (bounded) on rank r's counter before
+// its first load of those rows, so the local rows are multiplied while the peers' arrive.
 //
 // Grouped mode (MoE experts): the A operand is the expert-sorted token rows and B stacks the
 // experts' weights [E * N, K].  A device tile list, written by the routing kernels, gives
@@ -58,7 +65,30 @@ struct GemmParams {
   int grouped;
   const int4* gtiles;  // [entries] (expert, first row, end row, unused)
   const int* gcount;   // number of valid entries
+  GemmSPArgs sp;       // sequence-parallel all-gather wait / reduce-scatter epilogue
 };
+
+// Bounded wait until a monotonic counter (written by a peer with a system-scope release)
+// reaches `target`; returns at once once the status word is set (peers out of step).
+__device__ __forceinline__ bool gemm_wait_ctr(const unsigned int* c, unsigned int target,
+                                              uint32_t* status) {
+  auto ld = [](const unsigned int* q) {
+    unsigned int v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(q) : "memory");
+    return v;
+  };
+  if ((int)(ld(c) - target) >= 0) return true;
+  if (status != nullptr && *reinterpret_cast<volatile uint32_t*>(status) != 0u) return false;
+  const uint64_t t0 = globaltimer_ns();
+  while ((int)(ld(c) - target) < 0) {
+    if (globaltimer_ns() - t0 > B200_WAIT_TIMEOUT_NS) {
+      set_status(status, kTimeoutPeerFlag);
+      return false;
+    }
+    __nanosleep(64);
+  }
+  return true;
+}
 
 // Row coordinates of tile `mb` (an m-block index, or a tile-list entry in grouped mode).
 struct TileRows {
@@ -169,6 +199,7 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* tempty_bar = tfull_bar + 2;
   uint32_t* tmem_base_smem = reinterpret_cast<uint32_t*>(tempty_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_smem + 1);
+  unsigned int* rs_arrivals = tmem_base_smem + 2;  // epilogue threads done with their RS stores
 
   const int warp = warp_id();
   const int lane = lane_id();
@@ -185,6 +216,7 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&tempty_bar[a], 4);
     }
     *abort_flag = 0;
+    *rs_arrivals = 0u;
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -204,9 +236,23 @@ __global__ void __launch_bounds__(192, 1)
                                          : policy_evict_last();
       const uint64_t hint_b = kWeightIsA ? policy_evict_last()   // B = activations, reused
                                          : policy_evict_first();
+      uint32_t ag_ready = 0;  // ranks whose all-gathered A rows are known complete
       auto load_a = [&](int s, int kb, int mb) {
-        tma_load_2d(&tmA, &full_bar[s], smA + s * kATileBytes, kb * kBK, tile_rows(p, mb).a_row,
-                    hint_a);
+        const int a_row = tile_rows(p, mb).a_row;
+        if (p.sp.ag_ctr != nullptr) {
+          const int r0 = a_row / p.sp.ag_rows;
+          const int r1 = min(min(a_row + kBM - 1, p.M - 1) / p.sp.ag_rows, p.sp.ag_world - 1);
+          bool waited = false;
+          for (int r = r0; r <= r1; ++r) {
+            if (ag_ready & (1u << r)) continue;
+            gemm_wait_ctr(p.sp.ag_ctr + r, p.sp.ag_target[r], p.status);
+            ag_ready |= 1u << r;
+            waited = true;
+          }
+          // peer stores (generic proxy) -> this thread's TMA reads (async proxy)
+          if (waited) asm volatile("fence.proxy.async.global;" ::: "memory");
+        }
+        tma_load_2d(&tmA, &full_bar[s], smA + s * kATileBytes, kb * kBK, a_row, hint_a);
       };
       auto load_b = [&](int s, int kb, int nb, int mb) {
         const int base = p.grouped ? tile_rows(p, mb).b_base : 0;
@@ -373,10 +419,15 @@ __global__ void __launch_bounds__(192, 1)
           tmem_ld_32x32b_x32(t_row + c, r);
           tmem_ld_wait();
           const int n0 = n_base + c;
-          if constexpr (EPI == EPI_BF16) {
+          if constexpr (EPI == EPI_BF16 || EPI == EPI_BF16_RS) {
             if (m < m_lim) {
-              __nv_bfloat16* o =
-                  reinterpret_cast<__nv_bfloat16*>(p.out) + (long long)m * p.ldo + n0;
+              __nv_bfloat16* o;
+              if constexpr (EPI == EPI_BF16_RS) {
+                const int owner = m / p.sp.rs_rows;
+                o = p.sp.rs_out[owner] + (long long)(m - owner * p.sp.rs_rows) * p.ldo + n0;
+              } else {
+                o = reinterpret_cast<__nv_bfloat16*>(p.out) + (long long)m * p.ldo + n0;
+              }
               if (n0 + 32 <= p.N && (p.ldo % 8) == 0) {
                 uint4* dst = reinterpret_cast<uint4*>(o);
 #pragma unroll
@@ -423,6 +474,20 @@ __global__ void __launch_bounds__(192, 1)
                 if (n0 + j < p.N) atomicAdd(o + (long long)(n0 + j) * p.ldo, __uint_as_float(r[j]));
             }
           }
+        }
+      }
+      if constexpr (EPI == EPI_BF16_RS) {
+        // Every epilogue thread fences its own peer stores of this tile and arrives on a
+        // shared-memory counter; the 128th arrival raises the owners' counters (no blocking
+        // barrier, so a warp that left early on a failed wait cannot stall the others).
+        __threadfence_system();
+        const unsigned int prev = atomicAdd(rs_arrivals, 1u);
+        if (prev == 128u * (unsigned int)(t_local + 1) - 1u) {
+          __threadfence_system();
+          const int r0 = trows.a_row / p.sp.rs_rows;
+          const int r1 = min(trows.a_row + kBM - 1, p.M - 1) / p.sp.rs_rows;
+          for (int r = r0; r <= r1; ++r)
+            asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(p.sp.rs_ctr[r]) : "memory");
         }
       }
       tc_fence_before();
@@ -544,6 +609,17 @@ void gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
   if ((p.splits > 1 || p.streamk) && (a.epi != EPI_F32_RED && a.epi != EPI_F32_RED_T))
     throw std::invalid_argument("gemm: split-K / stream-K require an fp32 reduction epilogue");
   p.group_m = a.group_m > 0 ? a.group_m : 16;
+  p.sp = a.sp != nullptr ? *a.sp : GemmSPArgs{};
+  if (a.epi == EPI_BF16_RS && (a.sp == nullptr || a.sp->rs_rows <= 0 || grouped || p.splits > 1 ||
+                               p.streamk))
+    throw std::invalid_argument("gemm: the reduce-scatter epilogue needs SP args and no split-K");
+  if (p.sp.ag_ctr != nullptr && (p.sp.ag_rows <= 0 || p.sp.ag_world < 1 ||
+                                 p.sp.ag_world > kGemmMaxRanks ||
+                                 (long long)p.sp.ag_rows * p.sp.ag_world < a.M))
+    throw std::invalid_argument("gemm: bad all-gather layout");
+  if (a.epi == EPI_BF16_RS &&
+      ((long long)p.sp.rs_rows * kGemmMaxRanks < a.M || (a.M + p.sp.rs_rows - 1) / p.sp.rs_rows > kGemmMaxRanks))
+    throw std::invalid_argument("gemm: bad reduce-scatter layout");
   p.out = a.out;
   p.ldo = a.ldo;
   p.status = a.status;
@@ -566,6 +642,8 @@ void gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
   B200_GEMM_CASE(256, 4, EPI_BF16)
   B200_GEMM_CASE(128, 6, EPI_BF16)
   B200_GEMM_CASE(256, 4, EPI_SILU_BF16)
+  B200_GEMM_CASE(256, 4, EPI_BF16_RS)
+  B200_GEMM_CASE(128, 6, EPI_BF16_RS)
   B200_GEMM_CASE(128, 6, EPI_F32_RED)
   B200_GEMM_CASE(256, 4, EPI_F32_RED)
   B200_GEMM_CASE(16, 8, EPI_BF16_T)

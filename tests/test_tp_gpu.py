@@ -37,6 +37,8 @@ from vllm_neuron_b200.ops._ext import ext
 torch.cuda.synchronize()
 assert ext().read_status() == 0, "a bounded peer wait expired"
 assert llm.engine.model.sp_forwards > 0 or not sp, "sequence-parallel prefill did not run"
+spf = llm.engine.model.sp_fused
+assert not (fused and sp) or (spf is not None and spf.forwards > 0), "fused SP collectives did not run"
 if int(os.environ["RANK"]) == 0:
     json.dump([o.outputs[0].token_ids for o in outs], open(out_path, "w"))
 llm.shutdown()
@@ -80,7 +82,7 @@ def _run_tp(ckpt, world, fused, sp=False):
     return json.load(open(out))
 
 
-@pytest.mark.parametrize("fused,sp", [(False, False), (True, False), (True, True)])
+@pytest.mark.parametrize("fused,sp", [(False, False), (True, False), (False, True), (True, True)])
 def test_tp2_matches_tp1(ckpt, fused, sp):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")

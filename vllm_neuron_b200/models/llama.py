@@ -123,6 +123,8 @@ class LlamaForCausalLM(torch.nn.Module):
         self.sequence_parallel = False  # prefill residual stream sharded over tokens (TP > 1)
         self.mrope_section = None       # (t, h, w) frequency split of the multimodal RoPE
         self._sp = None                 # (padded tokens, local tokens) of the running SP forward
+        self.sp_fused = None            # SPFusedComm: fused SP collectives (CUDA, TP > 1)
+        self._spf = False               # the running forward uses sp_fused
         self.sp_forwards = 0            # forwards that ran sequence-parallel
         # Hidden states captured after these layers (EAGLE3 drafting): [tokens, len * H]
         self.aux_layers: list[int] = []
@@ -196,6 +198,14 @@ class LlamaForCausalLM(torch.nn.Module):
             from ..parallel.fused import TPFusedComm
 
             self.tp_fused = TPFusedComm(self.tp, self.H, self.max_decode_tokens, self.device, cpu_group)
+            # Sequence-parallel prefill with the all-gather / reduce-scatter fused into the GEMMs
+            # and the norm: dense SwiGLU decoders without an o_proj bias
+            if (self.sequence_parallel and type(self)._mlp is LlamaForCausalLM._mlp
+                    and all(getattr(ly, "o_bias", None) is None for ly in self.layers)):
+                from ..parallel.fused import SPFusedComm
+
+                self.sp_fused = SPFusedComm(self.tp, self.H, self.max_tokens + self.tp.world, self.device,
+                                            cpu_group)
 
     @property
     def num_kv_layers(self) -> int:
@@ -267,7 +277,11 @@ class LlamaForCausalLM(torch.nn.Module):
                                   qkv_bias=self._f32(ly, "qkv_bias"), positions3=b.positions3,
                                   mrope_section=self.mrope_section, k_scale=ks, v_scale=vs)
             else:
-                qkv = L.gemm_out(x[:T], ly.qkv, out=self.ws_qkv[:T])
+                if self._spf:
+                    qkv = self.sp_fused.gemm_ag(x[:T], ly.qkv, self.ws_qkv[:T], L.EPI_BF16,
+                                                L._pick_bn_wide(T, ly.qkv.shape[0], L.num_sms(x.device)))
+                else:
+                    qkv = L.gemm_out(x[:T], ly.qkv, out=self.ws_qkv[:T])
                 ops.rope_kv_write(qkv, b.positions, self.cos_sin, self.Hq, self.Hkv, self.D, q,
                                   k_cache, v_cache, b.slot_mapping, ly.q_norm, ly.k_norm, self.eps,
                                   rot_dim=self.cfg.rot_dim, q_pos_scale=self.q_pos_scale,
@@ -286,13 +300,18 @@ class LlamaForCausalLM(torch.nn.Module):
             else:
                 if Tg > T:
                     self.ws_attn[T:Tg].zero_()
-                h = L.gemm_out(self.ws_attn[:Tg], ly.o, out=self.ws_h[:Tg])
-                if ly.o_bias is not None and tp.rank == 0:
-                    h.add_(ly.o_bias)
-                self._reduce_norm(h, res, nxt_norm, x)
+                if self._spf:
+                    x = self._gemm_rs_norm(self.ws_attn[:Tg], ly.o, res, nxt_norm)
+                else:
+                    h = L.gemm_out(self.ws_attn[:Tg], ly.o, out=self.ws_h[:Tg])
+                    if ly.o_bias is not None and tp.rank == 0:
+                        h.add_(ly.o_bias)
+                    self._reduce_norm(h, res, nxt_norm, x)
             # ---- MLP
             nxt_norm = self.layers[i + 1].input_norm if i + 1 < nL else self.final_norm
-            self._mlp(i, ly, x, res, nxt_norm, Tg, small, fused)
+            x_new = self._mlp(i, ly, x, res, nxt_norm, Tg, small, fused)
+            if x_new is not None:
+                x = x_new
             if b.deep_feats is not None and i < b.deep_feats.shape[0]:
                 # DeepStack: visual features join the residual stream of the image-token rows
                 r = b.deep_rows
@@ -302,9 +321,19 @@ class LlamaForCausalLM(torch.nn.Module):
                 j = self.aux_layers.index(i)
                 self.aux_hidden[:T, j * self.H:(j + 1) * self.H].copy_(res)
         self._sp = None
+        if self._spf:
+            self._spf = False
+            self.sp_fused.wait_gathered()  # the final norm's rows from every rank
+            self.sp_fused.forwards += 1
         if b.want_hidden:
             return x.index_select(0, b.logits_indices.long())
         return self.compute_logits(x, b.logits_indices)
+
+    def _gemm_rs_norm(self, a: torch.Tensor, w: torch.Tensor, res: torch.Tensor, norm_w: torch.Tensor) -> torch.Tensor:
+        """Fused SP row-parallel epilogue: GEMM reduce-scattered into the owners' slots, then
+        residual add + RMSNorm + all-gather push; returns the gathered normalized rows."""
+        self.sp_fused.gemm_rs(a, w, L._pick_bn_wide(a.shape[0], w.shape[0], L.num_sms(a.device)))
+        return self.sp_fused.norm_push(res, norm_w, self.eps, reduce=True)
 
     @staticmethod
     def _f32(ly, name: str) -> torch.Tensor | None:
@@ -354,6 +383,10 @@ class LlamaForCausalLM(torch.nn.Module):
             full[T:].zero_()
         res = self.ws_residual[:Tl]
         tp.reduce_scatter(full, out=res)
+        self._spf = self.sp_fused is not None and Tl <= self.sp_fused.Tl_max
+        if self._spf:
+            # RMSNorm + all-gather push of the local rows in one kernel
+            return res, self.sp_fused.norm_push(res, self.layers[0].input_norm, self.eps, reduce=False), Tg
         x_l = self.ws_sp_x[:Tl]
         ops.rmsnorm(res, self.layers[0].input_norm, self.eps, out=x_l)
         x = self.ws_x[:Tg]
@@ -391,6 +424,15 @@ class LlamaForCausalLM(torch.nn.Module):
             L.gemm_accumulate(act, ly.down, acc)
             self._allreduce_norm(acc, res, nxt_norm, x, fused)
         else:
+            if self._spf:
+                if self.silu_blk:
+                    act = self.sp_fused.gemm_ag(x, ly.gate_up, self.ws_act[:T], L.EPI_SILU_BF16, 2 * L.SILU_BLOCK)
+                else:
+                    gu = torch.empty(T, ly.gate_up.shape[0], dtype=x.dtype, device=x.device)
+                    self.sp_fused.gemm_ag(x, ly.gate_up, gu, L.EPI_BF16,
+                                          L._pick_bn_wide(T, ly.gate_up.shape[0], L.num_sms(x.device)))
+                    act = ops.silu_mul(gu, out=self.ws_act[:T])
+                return self._gemm_rs_norm(act, ly.down, res, nxt_norm)
             if self.silu_blk:
                 act = L.gemm_silu(x, ly.gate_up, out=self.ws_act[:T])
             else:
