@@ -43,6 +43,9 @@ class EngineArgs:
     async_scheduling: bool | None = None  # default: on for CUDA devices
     additional_config: dict = field(default_factory=dict)
     kv_cache_dtype: str = "auto"   # "auto" (model dtype) | "fp8" / "fp8_e4m3" (per-layer scales)
+    # disaggregated prefill / decode: {"kv_role": "kv_producer" | "kv_consumer",
+    # "kv_connector": "TorchDistConnector", "kv_peer_rank": r}
+    kv_transfer_config: dict | None = None
     # {"method": "ngram" | "eagle3", "num_speculative_tokens": k, "model": draft checkpoint,
     #  "prompt_lookup_min"/"prompt_lookup_max": n-gram sizes}
     speculative_config: dict | None = None
@@ -182,6 +185,16 @@ class LLMEngine:
                                  else bool(args.async_scheduling))
         self._inflight = None  # (SchedulerOutput, StepHandle) of the launched, unprocessed step
         self._free_slots = list(range(self.runner.max_slots - 2, -1, -1))
+        self.kv_connector = None
+        from ..kv_transfer import KVTransferConfig, TorchDistKVConnector
+
+        self.kv_transfer = KVTransferConfig.coerce(args.kv_transfer_config)
+        if self.kv_transfer is not None:
+            if hasattr(self.model, "conv_state") or not hasattr(self.model, "kv_caches"):
+                raise NotImplementedError("KV transfer supports attention-only (KV cache) models")
+            from ..parallel import state as _ps
+
+            self.kv_connector = TorchDistKVConnector(self.kv_transfer, meta_group=_ps.get_parallel_state().cpu)
         self.tokenizer = None          # set by the LLM front end when it loads one
         self.structured_vocab = None   # token strings, for grammars on token-id-only engines
         self._structured = None
@@ -272,6 +285,51 @@ class LLMEngine:
                 self.block_manager.free_request(r)
                 self._free_slots.append(r.slot)
 
+    # ---------------------------------------------------------------- disaggregated prefill
+    def _send_remote(self, req: Request):
+        """Hand a finished request to the decode engine: its tokens and the KV of every token
+        but the last (whose KV the decode engine computes in its first step).  The blocks were
+        just freed by the scheduler; no later step has been scheduled onto them yet."""
+        bs = self.args.block_size
+        n_kv = req.num_tokens - 1
+        blocks = getattr(req, "freed_block_ids", req.block_ids)[:(n_kv + bs - 1) // bs]
+        kv = self.kv_connector.gather_kv(self.model.kv_caches, blocks)
+        meta = {"request_id": req.request_id, "prompt_token_ids": req.prompt_token_ids,
+                "output_token_ids": list(req.output_token_ids), "num_kv_tokens": n_kv}
+        self.kv_connector.send_request(meta, kv)
+
+    def recv_remote(self, params=None) -> Request:
+        """Receive one request from the prefill engine, install its KV into this engine's cache
+        and continue it as a running decode.  ``params``: the decode's SamplingParams, or a
+        callable (or dict) giving them from the request id.  Returns the request (already
+        finished when the prefill engine's tokens reached a stop condition)."""
+        meta, kv = self.kv_connector.recv_request(self.device)
+        if isinstance(params, dict):
+            params = params.get(meta["request_id"])
+        elif callable(params):
+            params = params(meta["request_id"])
+        params = SamplingParams.coerce(params)
+        req = Request(meta["request_id"], list(meta["prompt_token_ids"]), params, eos_token_id=self.eos_token_id)
+        req.output_token_ids = list(meta["output_token_ids"])
+        n_kv = int(meta["num_kv_tokens"])
+        if not self._free_slots:
+            raise RuntimeError("too many unfinished requests for the device token slots")
+        if not self.block_manager.allocate(req, n_kv):
+            raise RuntimeError("not enough free KV blocks for a transferred request")
+        self.kv_connector.scatter_kv(self.model.kv_caches, req.block_ids, kv)
+        req.num_computed_tokens = n_kv
+        now = time.perf_counter()
+        req.first_token_time = now
+        if req.check_stop(self.max_model_len):
+            req.finish_time = now
+            self.block_manager.free_request(req)
+            return req
+        req.slot = self._free_slots.pop()
+        req.status = RequestStatus.RUNNING
+        self.scheduler.requests[req.request_id] = req
+        self.scheduler.running.append(req)
+        return req
+
     def has_unfinished_requests(self) -> bool:
         return self.scheduler.has_unfinished() or self._inflight is not None
 
@@ -289,6 +347,8 @@ class LLMEngine:
             if req.slot >= 0 and req.num_pending == 0:
                 self._free_slots.append(req.slot)
                 req.slot = -1
+            if self.kv_connector is not None and self.kv_transfer.is_producer:
+                self._send_remote(req)
         # requests that stopped earlier and just received their last in-flight token
         for s in out.scheduled:
             r = s.req

@@ -243,6 +243,7 @@ class Scheduler:
         for req in finished:
             if req in self.running:
                 self.running.remove(req)
+            req.freed_block_ids = list(req.block_ids)  # KV hand-off (disaggregated prefill)
             self.bm.free_request(req)
             self.requests.pop(req.request_id, None)
         return finished
@@ -278,6 +279,7 @@ class Scheduler:
         for req in finished:
             if req in self.running:
                 self.running.remove(req)
+            req.freed_block_ids = list(req.block_ids)  # KV hand-off (disaggregated prefill)
             self.bm.free_request(req)
             self.requests.pop(req.request_id, None)
         return finished

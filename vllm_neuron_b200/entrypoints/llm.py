@@ -52,7 +52,8 @@ class LLM:
                  enforce_eager: bool = False, device: str | None = None, dtype: str = "auto",
                  async_scheduling: bool | None = None, speculative_config: dict | None = None,
                  data_parallel_size: int | None = None, mm_processor_kwargs: dict | None = None,
-                 kv_cache_dtype: str = "auto", enable_expert_parallel: bool = False, **unused):
+                 kv_cache_dtype: str = "auto", enable_expert_parallel: bool = False,
+                 kv_transfer_config: dict | None = None, **unused):
         if device is None:
             device = f"cuda:{torch.cuda.current_device()}" if torch.cuda.is_available() else "cpu"
         ps.init_distributed(backend="gloo" if str(device).startswith("cpu") else None)
@@ -71,6 +72,12 @@ class LLM:
         # parallel replicas, docs/design/parallelism/data_parallelism.md).
         self.dp_size = dp
         self.dp_rank = (torch.distributed.get_rank() // tensor_parallel_size) if world > 1 else 0
+        if kv_transfer_config is not None:
+            # disaggregated prefill / decode: each rank is its own engine (a prefill or a decode
+            # instance); the world only carries the KV hand-off
+            if tensor_parallel_size != 1:
+                raise NotImplementedError("KV transfer engines run with tensor_parallel_size=1")
+            self.dp_size, self.dp_rank = 1, 0
         self._dp_group = st.dp_cpu
         # Wide expert parallelism: with data-parallel replicas, an all-to-all backend and
         # enable_expert_parallel, MoE experts are sharded over every rank and tokens move by
@@ -86,7 +93,8 @@ class LLM:
                           load_format=load_format, seed=seed, dtype=dtype, device=device,
                           cuda_graphs=not enforce_eager, async_scheduling=async_scheduling,
                           additional_config=additional_config or {},
-                          speculative_config=speculative_config, kv_cache_dtype=kv_cache_dtype)
+                          speculative_config=speculative_config, kv_cache_dtype=kv_cache_dtype,
+                          kv_transfer_config=kv_transfer_config)
         self.engine = LLMEngine(args, tp=st.tp)
         self.mm_processor_kwargs = mm_processor_kwargs
         self.tokenizer = None
@@ -129,6 +137,27 @@ class LLM:
             for i, o in zip(idx, outs):
                 res[i] = o
         return res
+
+    def generate_remote(self, num_requests: int, sampling_params=None) -> list[RequestOutput]:
+        """Decode engine of a disaggregated pair: receive ``num_requests`` requests (prompt, the
+        prefill engine's tokens and their KV) and decode them to completion.
+        ``sampling_params``: one SamplingParams for all, or a dict / callable from request id
+        (a routing proxy knows each request's decode parameters).  Outputs are in arrival order
+        and include the tokens the prefill engine sampled."""
+        if self.engine.kv_connector is None or not self.engine.kv_transfer.is_consumer:
+            raise RuntimeError("generate_remote needs kv_transfer_config with kv_role='kv_consumer'")
+        reqs = [self.engine.recv_remote(sampling_params) for _ in range(num_requests)]
+        done = {r.request_id: r for r in reqs if r.status.finished}
+        for r in self.engine.run_until_done():
+            done[r.request_id] = r
+        outs = []
+        for r in reqs:
+            o = LLMEngine.to_output(done[r.request_id])
+            if self.tokenizer is not None:
+                for c in o.outputs:
+                    c.text = self.tokenizer.decode(c.token_ids, skip_special_tokens=True)
+            outs.append(o)
+        return outs
 
     def _generate(self, prompts, sampling_params, lockstep=None) -> list[RequestOutput]:
         ids = []
