@@ -1,0 +1,83 @@
+"""Encoder disaggregation on CPU: rank 0 is an encoder instance running Qwen3-VL's vision
+encoder for the image requests and sending the embeddings; rank 1 serves the requests with
+those embeddings instead of running its own encoder.  Greedy outputs equal a single engine's."""
+import multiprocessing as mp
+import os
+import socket
+
+import numpy as np
+
+from tests.test_qwen3_vl_cpu import IMG, PROC, VE, VS, _ckpt
+
+KW = dict(device="cpu", dtype="float32", max_num_seqs=2, max_model_len=256, num_gpu_blocks=64,
+          max_num_batched_tokens=8, mm_processor_kwargs=PROC, skip_tokenizer_init=True)
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _prompts():
+    rng = np.random.default_rng(1)
+    imgs = [(rng.random((24, 16, 3)) * 255).astype(np.uint8), (rng.random((16, 32, 3)) * 255).astype(np.uint8)]
+    return [{"prompt_token_ids": [7, 8, VS, IMG, VE, 9, 10], "multi_modal_data": {"image": imgs[0]}},
+            {"prompt_token_ids": [3, 4, 5, 6]},
+            {"prompt_token_ids": [11, VS, IMG, VE, 12], "multi_modal_data": {"image": imgs[1]}}]
+
+
+def _worker(rank, port, ckpt, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE="2",
+                      LOCAL_RANK=str(rank))
+    import torch
+
+    torch.set_num_threads(1)
+    from vllm_neuron_b200.engine.sampling_params import SamplingParams
+    from vllm_neuron_b200.entrypoints import LLM
+    from vllm_neuron_b200.parallel import state as ps
+
+    try:
+        role = "ec_producer" if rank == 0 else "ec_consumer"
+        llm = LLM(ckpt, ec_transfer_config={"ec_role": role}, **KW)
+        if rank == 0:
+            q.put((rank, llm.encode_remote(_prompts())))
+        else:
+            calls = []
+            vis = llm.engine.model.visual
+            orig = vis.forward
+            vis.forward = lambda *a, **k: (calls.append(1), orig(*a, **k))[1]
+            outs = llm.generate(_prompts(), SamplingParams(temperature=0, max_tokens=6, ignore_eos=True))
+            q.put((rank, ([o.outputs[0].token_ids for o in outs], len(calls))))
+    except Exception:  # pragma: no cover - reported to the parent
+        import traceback
+
+        q.put((rank, traceback.format_exc()))
+    finally:
+        ps.destroy_parallel_state()
+
+
+def test_encoder_disaggregation_matches_single_engine():
+    from vllm_neuron_b200.engine.sampling_params import SamplingParams
+    from vllm_neuron_b200.entrypoints import LLM
+
+    d, _ = _ckpt()
+    ref = LLM(d, **KW).generate(_prompts(), SamplingParams(temperature=0, max_tokens=6, ignore_eos=True))
+    ref = [o.outputs[0].token_ids for o in ref]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_worker, args=(r, port, d, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    for r in (1, 0):
+        assert not isinstance(res[r], str), res[r]
+    assert res[0] == 2
+    toks, encoder_calls = res[1]
+    assert toks == ref, (toks, ref)
+    assert encoder_calls == 0  # the serving instance never ran its vision encoder

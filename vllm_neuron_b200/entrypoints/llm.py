@@ -53,7 +53,8 @@ class LLM:
                  async_scheduling: bool | None = None, speculative_config: dict | None = None,
                  data_parallel_size: int | None = None, mm_processor_kwargs: dict | None = None,
                  kv_cache_dtype: str = "auto", enable_expert_parallel: bool = False,
-                 kv_transfer_config: dict | None = None, **unused):
+                 kv_transfer_config: dict | None = None, ec_transfer_config: dict | None = None,
+                 **unused):
         if device is None:
             device = f"cuda:{torch.cuda.current_device()}" if torch.cuda.is_available() else "cpu"
         ps.init_distributed(backend="gloo" if str(device).startswith("cpu") else None)
@@ -72,7 +73,15 @@ class LLM:
         # parallel replicas, docs/design/parallelism/data_parallelism.md).
         self.dp_size = dp
         self.dp_rank = (torch.distributed.get_rank() // tensor_parallel_size) if world > 1 else 0
-        if kv_transfer_config is not None:
+        self._ec = None
+        if ec_transfer_config is not None:
+            # encoder disaggregation: this rank is an encoder instance or a prefill/decode
+            # instance receiving vision embeddings (reference: EPD, the EC connector)
+            from ..kv_transfer import ECTransferConfig, TensorChannel
+
+            ecc = ECTransferConfig.coerce(ec_transfer_config)
+            self._ec = (ecc, TensorChannel(ecc.ec_peer_rank, meta_group=st.cpu))
+        if kv_transfer_config is not None or ec_transfer_config is not None:
             # disaggregated prefill / decode: each rank is its own engine (a prefill or a decode
             # instance); the world only carries the KV hand-off
             if tensor_parallel_size != 1:
@@ -138,6 +147,43 @@ class LLM:
                 res[i] = o
         return res
 
+    # ------------------------------------------------------------ encoder disaggregation
+    @staticmethod
+    def _mm_hash(mm) -> str:
+        import hashlib
+
+        return hashlib.sha1(mm.pixels.float().contiguous().numpy().tobytes()).hexdigest()
+
+    @torch.no_grad()
+    def encode_remote(self, prompts) -> int:
+        """Encoder instance: run the vision encoder of every image prompt and send the merged
+        embeddings (and DeepStack features) to the prefill/decode instance, in prompt order.
+        Returns the number of encodings sent."""
+        from ..engine.multimodal import prepare_image_request
+
+        if self._ec is None or self._ec[0].ec_role != "ec_producer":
+            raise RuntimeError("encode_remote needs ec_transfer_config with ec_role='ec_producer'")
+        sent = 0
+        dev = self.engine.device
+        for p in prompts:
+            if not (isinstance(p, dict) and p.get("multi_modal_data")):
+                continue
+            toks = _normalize_prompt(p, self.tokenizer)
+            _, mm = prepare_image_request(toks, p["multi_modal_data"].get("image"), self.engine.model,
+                                          self.engine.model_path, self.mm_processor_kwargs)
+            emb, deep = self.engine.model.encode_images(mm.pixels.to(dev), mm.grids)
+            deep = deep if deep is not None else torch.zeros(0, dtype=emb.dtype, device=dev)
+            self._ec[1].send({"mm_hash": self._mm_hash(mm)}, [emb, deep])
+            sent += 1
+        return sent
+
+    def _install_remote_encoding(self, mm):
+        meta, (emb, deep) = self._ec[1].recv(self.engine.device)
+        if meta["mm_hash"] != self._mm_hash(mm):
+            raise RuntimeError("received vision embeddings for a different image (requests out of order)")
+        mm.emb = emb
+        mm.deep = deep if deep.numel() else None
+
     def generate_remote(self, num_requests: int, sampling_params=None) -> list[RequestOutput]:
         """Decode engine of a disaggregated pair: receive ``num_requests`` requests (prompt, the
         prefill engine's tokens and their KV) and decode them to completion.
@@ -175,6 +221,8 @@ class LLM:
                 images = p["multi_modal_data"].get("image")
                 toks, mm = prepare_image_request(toks, images, self.engine.model, self.engine.model_path,
                                                  self.mm_processor_kwargs)
+                if self._ec is not None and self._ec[0].ec_role == "ec_consumer":
+                    self._install_remote_encoding(mm)
                 ids.append(self.engine.add_request(toks, sp, request_id=f"gen-{base}-{i}", mm=mm))
                 continue
             toks = _normalize_prompt(p, self.tokenizer)

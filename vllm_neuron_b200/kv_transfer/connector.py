@@ -102,3 +102,52 @@ class TorchDistKVConnector:
             kv = kv.view(dtype)
         self.received += 1
         return meta, kv
+
+
+@dataclass
+class ECTransferConfig:
+    """Encoder disaggregation: an encoder instance (``ec_producer``) runs the vision encoder of
+    image requests and sends the embeddings to a prefill/decode instance (``ec_consumer``)."""
+
+    ec_role: str = "ec_producer"
+    ec_peer_rank: int = -1
+
+    @classmethod
+    def coerce(cls, c) -> "ECTransferConfig | None":
+        if c is None or isinstance(c, cls):
+            return c
+        cfg = cls(**{k: v for k, v in dict(c).items() if k in ("ec_role", "ec_peer_rank")})
+        if cfg.ec_role not in ("ec_producer", "ec_consumer"):
+            raise ValueError(f"ec_role must be ec_producer or ec_consumer, got {cfg.ec_role!r}")
+        return cfg
+
+
+class TensorChannel:
+    """Point-to-point channel of (metadata, tensors) messages between two engine processes:
+    metadata through a gloo group, tensors through ``data_group`` (NCCL between GPUs, gloo on
+    CPU).  Reference: the EC connector (vllm_neuron/vllm/ec_connector/neuron_nixl_ec_connector.py)
+    moving encoder outputs between instances."""
+
+    def __init__(self, peer: int = -1, meta_group=None, data_group=None):
+        self.peer = peer if peer >= 0 else 1 - dist.get_rank()
+        self.meta_group = meta_group
+        self.data_group = data_group
+
+    def send(self, meta: dict, tensors: list[torch.Tensor]) -> None:
+        specs = [(list(t.shape), str(t.dtype).replace("torch.", "")) for t in tensors]
+        dist.send_object_list([dict(meta, _tensors=specs)], dst=self.peer, group=self.meta_group)
+        for t in tensors:
+            if t.numel():
+                dist.send(t.contiguous(), dst=self.peer, group=self.data_group)
+
+    def recv(self, device) -> tuple[dict, list[torch.Tensor]]:
+        box = [None]
+        dist.recv_object_list(box, src=self.peer, group=self.meta_group)
+        meta = box[0]
+        out = []
+        for shape, dt in meta.pop("_tensors"):
+            t = torch.empty(shape, dtype=getattr(torch, dt), device=device)
+            if t.numel():
+                dist.recv(t, src=self.peer, group=self.data_group)
+            out.append(t)
+        return meta, out
