@@ -81,3 +81,58 @@ def test_encoder_disaggregation_matches_single_engine():
     toks, encoder_calls = res[1]
     assert toks == ref, (toks, ref)
     assert encoder_calls == 0  # the serving instance never ran its vision encoder
+
+
+def _vision_dp_worker(rank, port, ckpt, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE="2",
+                      LOCAL_RANK=str(rank))
+    import torch
+
+    torch.set_num_threads(1)
+    from vllm_neuron_b200.engine.sampling_params import SamplingParams
+    from vllm_neuron_b200.entrypoints import LLM
+    from vllm_neuron_b200.parallel import state as ps
+
+    try:
+        llm = LLM(ckpt, tensor_parallel_size=2, **KW)
+        outs = llm.generate(_three_image_prompts(), SamplingParams(temperature=0, max_tokens=5, ignore_eos=True))
+        q.put((rank, ([o.outputs[0].token_ids for o in outs], llm.engine.model.vision_calls)))
+    except Exception:  # pragma: no cover
+        import traceback
+
+        q.put((rank, traceback.format_exc()))
+    finally:
+        ps.destroy_parallel_state()
+
+
+def _three_image_prompts():
+    rng = np.random.default_rng(2)
+    imgs = [(rng.random(s) * 255).astype(np.uint8) for s in ((24, 16, 3), (16, 32, 3), (16, 16, 3))]
+    return [{"prompt_token_ids": [7, VS, IMG, VE, 8, VS, IMG, VE, 9, VS, IMG, VE, 10],
+             "multi_modal_data": {"image": imgs}}]
+
+
+def test_vision_data_parallel_over_tp_ranks():
+    """TP=2: the request's three images are encoded 2 + 1 by the two ranks and gathered; the
+    tokens equal a TP=1 run (which encodes all three itself)."""
+    from vllm_neuron_b200.engine.sampling_params import SamplingParams
+    from vllm_neuron_b200.entrypoints import LLM
+
+    d, _ = _ckpt()
+    ref_llm = LLM(d, **KW)
+    ref = ref_llm.generate(_three_image_prompts(), SamplingParams(temperature=0, max_tokens=5, ignore_eos=True))
+    ref = [o.outputs[0].token_ids for o in ref]
+    assert ref_llm.engine.model.vision_calls == 3
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_vision_dp_worker, args=(r, port, d, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    for r in (0, 1):
+        assert not isinstance(res[r], str), res[r]
+    assert res[0][0] == ref and res[1][0] == ref, (res, ref)
+    assert res[0][1] == 2 and res[1][1] == 1

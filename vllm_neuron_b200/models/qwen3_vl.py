@@ -241,8 +241,57 @@ class Qwen3VLForConditionalGeneration(LlamaForCausalLM):
             else:
                 prm.normal_(0.0, std, generator=g)
 
+    vision_dp = True  # split a request's images over the TP ranks (vision data parallelism)
+    vision_calls = 0  # images encoded by this rank (observability / tests)
+
     def encode_images(self, pixels: torch.Tensor, grids: list[tuple[int, int, int]]):
-        return self.visual(pixels, grids)
+        """Merged vision embeddings ``[tokens, H]`` and DeepStack features ``[n_deep, tokens, H]``
+        of the images of one request, in image order.
+
+        Vision data parallelism: with TP > 1 and several images, image ``i`` is encoded by TP
+        rank ``i % W`` only (the vision weights are replicated) and the results are all-gathered
+        (padded to the largest share), instead of every rank encoding every image.  Reference:
+        the vision TP/DP groups (vllm_neuron/parallel/neuron_parallel_state.py:667-701; vision
+        DP defaults to the world, vllm_neuron/model/neuron_config.py:345-404)."""
+        W = self.tp.world
+        if W == 1 or len(grids) < 2 or not self.vision_dp:
+            self.vision_calls += len(grids)
+            return self.visual(pixels, grids)
+        m2 = self.spatial_merge ** 2
+        counts = [t * h * w for t, h, w in grids]
+        starts = [sum(counts[:i]) for i in range(len(grids))]
+        rows = [c // m2 for c in counts]
+        owner = [i % W for i in range(len(grids))]
+        mine = [i for i in range(len(grids)) if owner[i] == self.tp.rank]
+        H = self.H
+        if mine:
+            px = torch.cat([pixels[starts[i]:starts[i] + counts[i]] for i in mine])
+            emb, deep = self.visual(px, [grids[i] for i in mine])
+            self.vision_calls += len(mine)
+        else:
+            emb, deep = pixels.new_zeros(0, H, dtype=self.dtype), None
+        nd = len(self.visual.deep_idx)  # same on every rank, also those without an image
+        share = [sum(rows[i] for i in range(len(grids)) if owner[i] == r) for r in range(W)]
+        R = max(share)
+        pack = torch.zeros(R, H * (1 + nd), dtype=emb.dtype, device=emb.device)
+        n = emb.shape[0]
+        pack[:n, :H] = emb
+        if nd:
+            pack[:n, H:] = deep.permute(1, 0, 2).reshape(n, nd * H).to(emb.dtype)
+        allp = self.tp.all_gather(pack.unsqueeze(0), dim=0)          # [W, R, H * (1 + nd)]
+        offs = [0] * W
+        e_parts, d_parts = [], []
+        for i in range(len(grids)):
+            r = owner[i]
+            blk = allp[r, offs[r]:offs[r] + rows[i]]
+            offs[r] += rows[i]
+            e_parts.append(blk[:, :H])
+            if nd:
+                d_parts.append(blk[:, H:].reshape(rows[i], nd, H))
+        emb_all = torch.cat(e_parts)
+        deep_all = (torch.cat(d_parts).permute(1, 0, 2).contiguous() if nd
+                    else emb_all.new_zeros(0, emb_all.shape[0], H))
+        return emb_all, deep_all
 
     def load_hf_state_dict(self, get_tensor, names: set[str]):
         from ..utils.weight_loader import load_dense_decoder, load_qwen3_vl_vision
