@@ -110,6 +110,73 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, int64_t epi
 
 static void fill_ptrs(const std::vector<int64_t>& v, void** dst, const char* what);
 
+// FP8 (e4m3) GEMM with per-tensor scales: out = alpha * (a @ b^T) (epilogue as in `gemm`).
+void gemm_fp8(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, int64_t epi, int64_t bn,
+              int64_t splits, double alpha) {
+  CHECK_CUDA(a);
+  CHECK_CUDA(b);
+  TORCH_CHECK(a.scalar_type() == at::kFloat8_e4m3fn && b.scalar_type() == at::kFloat8_e4m3fn,
+              "gemm_fp8: operands must be float8_e4m3fn");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.size(1) == b.size(1), "gemm_fp8: bad shapes");
+  TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1 && out.stride(-1) == 1,
+              "gemm_fp8: inner dims must be contiguous");
+  const bool f32_out = (epi == b200::EPI_F32_RED || epi == b200::EPI_F32_RED_T);
+  TORCH_CHECK(out.scalar_type() == (f32_out ? at::kFloat : at::kBFloat16), "gemm_fp8: out dtype");
+  const c10::cuda::CUDAGuard guard(a.device());
+  b200::GemmArgs g{};
+  g.A = a.data_ptr();
+  g.B = b.data_ptr();
+  g.out = out.data_ptr();
+  g.lda = a.stride(0);
+  g.ldb = b.stride(0);
+  g.ldo = out.stride(0);
+  g.M = (int)a.size(0);
+  g.N = (int)b.size(0);
+  g.K = (int)a.size(1);
+  g.bn = (int)bn;
+  g.epi = (int)epi;
+  g.splits = (int)splits;
+  g.status = status_word();
+  g.fp8 = 1;
+  g.alpha = (float)alpha;
+  if (g.M == 0 || g.N == 0) return;
+  b200::gemm_bf16_launch(g, cur_stream());
+  check_launch("gemm_fp8");
+}
+
+void quant_fp8(const at::Tensor& x, at::Tensor& out, double inv_scale) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  TORCH_CHECK(out.scalar_type() == at::kFloat8_e4m3fn && x.dim() == 2 && out.sizes() == x.sizes() &&
+                  x.stride(1) == 1 && out.stride(1) == 1, "quant_fp8: layouts");
+  const c10::cuda::CUDAGuard guard(x.device());
+  b200::quant_fp8_launch(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0),
+                         reinterpret_cast<uint8_t*>(out.data_ptr()), out.stride(0), (int)x.size(0),
+                         (int)x.size(1), (float)inv_scale, cur_stream());
+  check_launch("quant_fp8", x.size(0) > 0 ? 1 : 0);
+}
+
+void rmsnorm_quant(const at::Tensor& x, const at::Tensor& w, double eps, at::Tensor& out,
+                   double inv_scale, c10::optional<at::Tensor> row_scales) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  CHECK_BF16(w);
+  TORCH_CHECK(out.scalar_type() == at::kFloat8_e4m3fn && x.dim() == 2 && out.sizes() == x.sizes() &&
+                  x.stride(1) == 1 && out.stride(1) == 1, "rmsnorm_quant: layouts");
+  float* rs = nullptr;
+  if (row_scales.has_value()) {
+    TORCH_CHECK(row_scales->scalar_type() == at::kFloat && row_scales->numel() >= x.size(0),
+                "rmsnorm_quant: row_scales must be fp32 [rows]");
+    rs = row_scales->data_ptr<float>();
+  }
+  const c10::cuda::CUDAGuard guard(x.device());
+  b200::rmsnorm_quant_launch(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0),
+                             reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), (float)eps,
+                             reinterpret_cast<uint8_t*>(out.data_ptr()), out.stride(0), (int)x.size(0),
+                             (int)x.size(1), (float)inv_scale, rs, cur_stream());
+  check_launch("rmsnorm_quant", x.size(0) > 0 ? 1 : 0);
+}
+
 // Sequence-parallel GEMM: optional all-gather wait on the A rows (ag_ctr != 0: local counter
 // array address, ag_targets per source rank, ag_rows rows per rank) and / or the reduce-scatter
 // epilogue (epi == EPI_BF16_RS: rs_out / rs_ctr peer addresses per owner rank, rs_rows rows per
@@ -792,6 +859,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels of vllm_neuron_b200";
   m.def("gemm", &gemm);
   m.def("gemm_sp", &gemm_sp);
+  m.def("gemm_fp8", &gemm_fp8);
+  m.def("quant_fp8", &quant_fp8);
+  m.def("rmsnorm_quant", &rmsnorm_quant);
   m.def("sp_norm_push", &sp_norm_push);
   m.def("sp_wait", &sp_wait);
   m.def("paged_attention", &paged_attention);

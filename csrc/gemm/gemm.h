@@ -54,6 +54,10 @@ struct GemmArgs {
   int gmax = 0;
   int num_groups = 0;
   const GemmSPArgs* sp = nullptr;  // sequence-parallel fusion (null: plain GEMM)
+  // FP8 (e4m3) operands: A and B hold bytes, K counts elements (multiple of 16), and the
+  // accumulator is multiplied by `alpha` (per-tensor scales a * b) in the epilogue.
+  int fp8 = 0;
+  float alpha = 1.f;
 };
 
 void gemm_bf16_launch(const GemmArgs& args, cudaStream_t stream);

@@ -33,6 +33,10 @@
 // entry's end row only.  Rows past the end of the block belong to the next expert (or are
 // TMA zero fill) and are discarded.
 //
+// FP8 (e4m3 x e4m3, per-tensor scales): tcgen05.mma kind::f8f6f4 on the same byte tiles, 128
+// elements per k-block, the accumulator scaled by alpha = scale_a * scale_b in the epilogue
+// (static W8A8 checkpoints: the reference's ModelOpt FP8 Llama, model/llama3/quantization.py).
+//
 // This is the B200 replacement of the dense projections that the reference runs through
 // its NKI qkv / mlp / output_projection kernels (vllm_neuron/functional/attention/qkv.py:672,
 // vllm_neuron/functional/mlp.py:65, vllm_neuron/functional/attention/o_proj.py:124).
@@ -66,6 +70,7 @@ struct GemmParams {
   const int4* gtiles;  // [entries] (expert, first row, end row, unused)
   const int* gcount;   // number of valid entries
   GemmSPArgs sp;       // sequence-parallel all-gather wait / reduce-scatter epilogue
+  float alpha;         // epilogue scale of FP8 operands (1 for bf16)
 };
 
 // Bounded wait until a monotonic counter (written by a peer with a system-scope release)
@@ -178,14 +183,18 @@ struct TmemCols {
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
 
-template <int BN, int STAGES, int EPI>
+// FP8 = true: e4m3 operands (kind::f8f6f4).  A 128-byte swizzle row then holds 128 elements, so
+// the shared-memory tiles and the per-instruction descriptor advance (32 bytes) are unchanged;
+// only the k-block element count, the MMA kind and the epilogue scale differ.
+template <int BN, int STAGES, int EPI, bool FP8 = false>
 __global__ void __launch_bounds__(192, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA,
                      const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
   constexpr int kBTileBytes = BN * kBK * 2;
   constexpr int kStageBytes = kATileBytes + kBTileBytes;
   constexpr uint32_t kTmemCols = TmemCols<BN>::v;
-  constexpr uint32_t kIdesc = make_idesc_f16(kBM, BN, true);
+  constexpr uint32_t kIdesc = make_idesc_f16(kBM, BN, !FP8);  // FP8: type fields 0 = E4M3
+  constexpr int kKElems = FP8 ? 2 * kBK : kBK;                  // elements per k-block
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the swizzled tiles.
@@ -252,11 +261,11 @@ __global__ void __launch_bounds__(192, 1)
           // peer stores (generic proxy) -> this thread's TMA reads (async proxy)
           if (waited) asm volatile("fence.proxy.async.global;" ::: "memory");
         }
-        tma_load_2d(&tmA, &full_bar[s], smA + s * kATileBytes, kb * kBK, a_row, hint_a);
+        tma_load_2d(&tmA, &full_bar[s], smA + s * kATileBytes, kb * kKElems, a_row, hint_a);
       };
       auto load_b = [&](int s, int kb, int nb, int mb) {
         const int base = p.grouped ? tile_rows(p, mb).b_base : 0;
-        tma_load_2d(&tmB, &full_bar[s], smB + s * kBTileBytes, kb * kBK, base + nb * BN, hint_b);
+        tma_load_2d(&tmB, &full_bar[s], smB + s * kBTileBytes, kb * kKElems, base + nb * BN, hint_b);
       };
       // The grouped tile list is written by the previous kernel.
       if (p.grouped) pdl_wait();
@@ -351,7 +360,10 @@ __global__ void __launch_bounds__(192, 1)
           for (int k = 0; k < kBK / 16; ++k) {
             const uint64_t adesc = make_sdesc_sw128(a_addr + k * 32);
             const uint64_t bdesc = make_sdesc_sw128(b_addr + k * 32);
-            umma_f16_ss(d_tmem, adesc, bdesc, kIdesc, (kb > k0 || k > 0) ? 1u : 0u);
+            if constexpr (FP8)
+              umma_f8_ss(d_tmem, adesc, bdesc, kIdesc, (kb > k0 || k > 0) ? 1u : 0u);
+            else
+              umma_f16_ss(d_tmem, adesc, bdesc, kIdesc, (kb > k0 || k > 0) ? 1u : 0u);
           }
           umma_commit(&empty_bar[s]);
         }
@@ -388,6 +400,13 @@ __global__ void __launch_bounds__(192, 1)
           tmem_ld_32x32b_x16(t_row + c, g);
           tmem_ld_32x32b_x16(t_row + H + c, u);
           tmem_ld_wait();
+          if constexpr (FP8) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              g[j] = __float_as_uint(__uint_as_float(g[j]) * p.alpha);
+              u[j] = __float_as_uint(__uint_as_float(u[j]) * p.alpha);
+            }
+          }
           if (m < m_lim) {
             __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + (long long)m * p.ldo;
             uint32_t packed[8];
@@ -418,6 +437,10 @@ __global__ void __launch_bounds__(192, 1)
           uint32_t r[32];
           tmem_ld_32x32b_x32(t_row + c, r);
           tmem_ld_wait();
+          if constexpr (FP8) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * p.alpha);
+          }
           const int n0 = n_base + c;
           if constexpr (EPI == EPI_BF16 || EPI == EPI_BF16_RS) {
             if (m < m_lim) {
@@ -559,11 +582,11 @@ CUtensorMap make_tmap_u8_2d(const void* ptr, uint64_t inner, uint64_t outer, uin
   return m;
 }
 
-template <int BN, int STAGES, int EPI>
+template <int BN, int STAGES, int EPI, bool FP8 = false>
 static void launch_impl(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
                         int grid, cudaStream_t stream) {
   constexpr int smem = STAGES * (kATileBytes + BN * kBK * 2) + 1024 + 256;
-  auto kern = gemm_bf16_kernel<BN, STAGES, EPI>;
+  auto kern = gemm_bf16_kernel<BN, STAGES, EPI, FP8>;
   static std::atomic<uint64_t> configured{0};  // per instantiation, per device
   set_max_dynamic_smem_once(kern, smem, configured);
   launch_pdl(kern, dim3(grid), dim3(192), smem, stream, ta, tb, p);
@@ -580,16 +603,22 @@ int num_sms_cached() {
 }
 
 void gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
-  if (a.K % 8 != 0) throw std::invalid_argument("gemm: K must be a multiple of 8");
-  if (a.lda % 8 != 0 || a.ldb % 8 != 0)
-    throw std::invalid_argument("gemm: row pitches must be multiples of 8 elements");
+  const int esz = a.fp8 ? 1 : 2;        // bytes per element
+  const int kelems = a.fp8 ? 2 * kBK : kBK;  // elements per 128-byte k-block
+  if ((a.K * esz) % 16 != 0) throw std::invalid_argument("gemm: K rows must be multiples of 16 bytes");
+  if ((a.lda * esz) % 16 != 0 || (a.ldb * esz) % 16 != 0)
+    throw std::invalid_argument("gemm: row pitches must be multiples of 16 bytes");
   const int bn = a.bn;
   const bool grouped = a.gtiles != nullptr;
   if (grouped && (a.splits > 1 || a.splits < 0 || a.num_groups < 1 || a.gmax < 1))
     throw std::invalid_argument("gemm: grouped mode needs splits == 1, groups and a tile bound");
-  const CUtensorMap ta = make_tmap_bf16_2d(a.A, a.K, a.M, a.lda, kBK, kBM, true);
-  const CUtensorMap tb = make_tmap_bf16_2d(a.B, a.K, grouped ? (uint64_t)a.N * a.num_groups : a.N,
-                                           a.ldb, kBK, bn, true);
+  if (a.fp8 && (grouped || a.sp != nullptr))
+    throw std::invalid_argument("gemm: FP8 operands are for the dense (non-grouped, non-SP) modes");
+  const uint64_t b_rows = grouped ? (uint64_t)a.N * a.num_groups : (uint64_t)a.N;
+  const CUtensorMap ta = a.fp8 ? make_tmap_u8_2d(a.A, a.K, a.M, a.lda, 128, kBM, 128)
+                               : make_tmap_bf16_2d(a.A, a.K, a.M, a.lda, kBK, kBM, true);
+  const CUtensorMap tb = a.fp8 ? make_tmap_u8_2d(a.B, a.K, b_rows, a.ldb, 128, bn, 128)
+                               : make_tmap_bf16_2d(a.B, a.K, b_rows, a.ldb, kBK, bn, true);
   GemmParams p;
   p.grouped = grouped ? 1 : 0;
   p.gtiles = reinterpret_cast<const int4*>(a.gtiles);
@@ -600,7 +629,8 @@ void gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
   p.num_m_blocks = (a.M + kBM - 1) / kBM;
   p.num_n_blocks = (a.N + bn - 1) / bn;
   if (a.epi == EPI_SILU_BF16) p.num_n_blocks = (a.N + bn - 1) / bn;  // N = 2 * I (interleaved)
-  p.num_k_blocks = (a.K + kBK - 1) / kBK;
+  p.num_k_blocks = (a.K + kelems - 1) / kelems;
+  p.alpha = a.fp8 ? a.alpha : 1.f;
   p.streamk = a.splits < 0 ? 1 : 0;
   int splits = a.splits < 1 ? 1 : a.splits;
   if (splits > p.num_k_blocks) splits = p.num_k_blocks;
@@ -634,6 +664,24 @@ void gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
     grid = (int)tiles;
   }
 
+#define B200_GEMM_FP8_CASE(BN_, ST_, EPI_)                                \
+  if (bn == BN_ && a.epi == EPI_) {                                       \
+    launch_impl<BN_, ST_, EPI_, true>(ta, tb, p, grid, stream);           \
+    return;                                                               \
+  }
+  if (a.fp8) {
+    B200_GEMM_FP8_CASE(256, 4, EPI_BF16)
+    B200_GEMM_FP8_CASE(128, 6, EPI_BF16)
+    B200_GEMM_FP8_CASE(256, 4, EPI_SILU_BF16)
+    B200_GEMM_FP8_CASE(128, 6, EPI_F32_RED)
+    B200_GEMM_FP8_CASE(16, 8, EPI_F32_RED_T)
+    B200_GEMM_FP8_CASE(32, 8, EPI_F32_RED_T)
+    B200_GEMM_FP8_CASE(64, 8, EPI_F32_RED_T)
+    B200_GEMM_FP8_CASE(128, 6, EPI_F32_RED_T)
+    throw std::invalid_argument("gemm (fp8): unsupported (bn, epilogue) combination: bn=" +
+                                std::to_string(bn) + " epi=" + std::to_string(a.epi));
+  }
+#undef B200_GEMM_FP8_CASE
 #define B200_GEMM_CASE(BN_, ST_, EPI_)                                    \
   if (bn == BN_ && a.epi == EPI_) {                                       \
     launch_impl<BN_, ST_, EPI_>(ta, tb, p, grid, stream);                 \

@@ -44,6 +44,14 @@ struct RopeKvParams {
 void rope_kv_write_launch(const RopeKvParams& p, void* qkv, bool qkv_is_f32, int T,
                           cudaStream_t stream);
 
+// FP8 (e4m3) activation quantization (quant.cu).
+void quant_fp8_launch(const __nv_bfloat16* x, long long ldx, uint8_t* out, long long ldo, int rows,
+                      int cols, float inv_scale, cudaStream_t stream);
+// row_scales == null: static per-tensor scale; else per-row dynamic scales (max|y| / 448).
+void rmsnorm_quant_launch(const __nv_bfloat16* x, long long ldx, const __nv_bfloat16* w, float eps,
+                          uint8_t* out, long long ldo, int rows, int H, float inv_scale,
+                          float* row_scales, cudaStream_t stream);
+
 void silu_mul_launch(void* in, bool in_is_f32, long long in_stride, __nv_bfloat16* out,
                      long long out_stride, int T, int I, int blk, bool clear_input, int act,
                      float limit, float alpha, cudaStream_t stream);

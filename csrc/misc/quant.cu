@@ -1,0 +1,153 @@
+// FP8 (e4m3) activation quantization for W8A8 GEMMs.
+//
+//   quant_fp8       out = satfinite(x * inv_scale) for bf16 rows (static per-tensor scale)
+//   rmsnorm_quant   y = rmsnorm(x) * w, then either the static per-tensor quantization above
+//                   (STATIC) or a per-row scale s_row = max|y| / 448 with out = y / s_row and
+//                   s_row written to `row_scales` (ROW)
+//
+// Reference: rmsnorm_quant (vllm_neuron/functional/rmsnorm_quant.py:216; STATIC and ROW modes,
+// the reference packs the row scale into 4 extra fp8 bytes, here it is a separate fp32 vector).
+// Conversion is the hardware cvt (__nv_cvt_float_to_fp8, satfinite, round to nearest even).
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+
+#include <stdexcept>
+
+#include "../common.cuh"
+#include "misc.h"
+
+namespace b200 {
+
+namespace {
+__device__ __forceinline__ uint32_t q4(float a, float b, float c, float d) {
+  return (uint32_t)__nv_cvt_float_to_fp8(a, __NV_SATFINITE, __NV_E4M3) |
+         ((uint32_t)__nv_cvt_float_to_fp8(b, __NV_SATFINITE, __NV_E4M3) << 8) |
+         ((uint32_t)__nv_cvt_float_to_fp8(c, __NV_SATFINITE, __NV_E4M3) << 16) |
+         ((uint32_t)__nv_cvt_float_to_fp8(d, __NV_SATFINITE, __NV_E4M3) << 24);
+}
+}  // namespace
+
+// grid (rows, ceil(cols / 2048)), 256 threads x 8 elements
+__global__ void __launch_bounds__(256) quant_fp8_kernel(const __nv_bfloat16* __restrict__ x,
+                                                        long long ldx, uint8_t* __restrict__ out,
+                                                        long long ldo, int cols, float inv_scale) {
+  pdl_trigger();
+  pdl_wait();
+  const long long r = blockIdx.x;
+  const int c = (blockIdx.y * 256 + threadIdx.x) * 8;
+  if (c >= cols) return;
+  const uint4 v = *reinterpret_cast<const uint4*>(x + r * ldx + c);
+  const float2 a = unpack_bf16x2(v.x), b = unpack_bf16x2(v.y), d = unpack_bf16x2(v.z),
+               e = unpack_bf16x2(v.w);
+  *reinterpret_cast<uint2*>(out + r * ldo + c) =
+      make_uint2(q4(a.x * inv_scale, a.y * inv_scale, b.x * inv_scale, b.y * inv_scale),
+                 q4(d.x * inv_scale, d.y * inv_scale, e.x * inv_scale, e.y * inv_scale));
+}
+
+// One CTA (256 threads) per row, H <= 8192.
+template <int NV>
+__global__ void __launch_bounds__(256) rmsnorm_quant_kernel(const __nv_bfloat16* __restrict__ x,
+                                                            long long ldx,
+                                                            const __nv_bfloat16* __restrict__ w,
+                                                            float eps, uint8_t* __restrict__ out,
+                                                            long long ldo, int H, float inv_scale,
+                                                            float* __restrict__ row_scales) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ float red[8];
+  __shared__ float redm[8];
+  const long long r = blockIdx.x;
+  const int tid = threadIdx.x;
+  float v[NV][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int idx = (j * 256 + tid) * 8;
+    if (idx < H) {
+      const uint4 u = *reinterpret_cast<const uint4*>(x + r * ldx + idx);
+      const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = unpack_bf16x2(uw[i]);
+        v[j][2 * i] = f.x;
+        v[j][2 * i + 1] = f.y;
+        ss += f.x * f.x + f.y * f.y;
+      }
+    }
+  }
+  ss = warp_sum(ss);
+  if ((tid & 31) == 0) red[tid >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) tot += red[i];
+  const float rstd = rsqrtf(tot / (float)H + eps);
+  float amax = 0.f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int idx = (j * 256 + tid) * 8;
+    if (idx < H) {
+      const uint4 u = *reinterpret_cast<const uint4*>(w + idx);
+      const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = unpack_bf16x2(uw[i]);
+        // the normalized value is rounded to bf16 before the weight (as the bf16 RMSNorm)
+        v[j][2 * i] = __bfloat162float(__float2bfloat16(v[j][2 * i] * rstd)) * f.x;
+        v[j][2 * i + 1] = __bfloat162float(__float2bfloat16(v[j][2 * i + 1] * rstd)) * f.y;
+        amax = fmaxf(amax, fmaxf(fabsf(v[j][2 * i]), fabsf(v[j][2 * i + 1])));
+      }
+    }
+  }
+  float inv = inv_scale;
+  if (row_scales != nullptr) {
+    amax = warp_max(amax);
+    if ((tid & 31) == 0) redm[tid >> 5] = amax;
+    __syncthreads();
+    float m = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m = fmaxf(m, redm[i]);
+    const float s = m > 0.f ? m / 448.f : 1.f;
+    inv = 1.f / s;
+    if (tid == 0) row_scales[r] = s;
+  }
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int idx = (j * 256 + tid) * 8;
+    if (idx < H)
+      *reinterpret_cast<uint2*>(out + r * ldo + idx) =
+          make_uint2(q4(v[j][0] * inv, v[j][1] * inv, v[j][2] * inv, v[j][3] * inv),
+                     q4(v[j][4] * inv, v[j][5] * inv, v[j][6] * inv, v[j][7] * inv));
+  }
+}
+
+void quant_fp8_launch(const __nv_bfloat16* x, long long ldx, uint8_t* out, long long ldo, int rows,
+                      int cols, float inv_scale, cudaStream_t stream) {
+  if (rows == 0) return;
+  if (cols % 8 != 0 || ldx % 8 != 0 || ldo % 8 != 0)
+    throw std::invalid_argument("quant_fp8: columns and row pitches must be multiples of 8");
+  launch_pdl(quant_fp8_kernel, dim3(rows, (cols + 2047) / 2048), dim3(256), 0, stream, x, ldx, out,
+             ldo, cols, inv_scale);
+}
+
+void rmsnorm_quant_launch(const __nv_bfloat16* x, long long ldx, const __nv_bfloat16* w, float eps,
+                          uint8_t* out, long long ldo, int rows, int H, float inv_scale,
+                          float* row_scales, cudaStream_t stream) {
+  if (rows == 0) return;
+  if (H % 8 != 0 || ldx % 8 != 0 || ldo % 8 != 0)
+    throw std::invalid_argument("rmsnorm_quant: H and row pitches must be multiples of 8");
+  const int nv = (H / 8 + 255) / 256;
+  if (nv == 1)
+    launch_pdl(rmsnorm_quant_kernel<1>, dim3(rows), dim3(256), 0, stream, x, ldx, w, eps, out, ldo,
+               H, inv_scale, row_scales);
+  else if (nv == 2)
+    launch_pdl(rmsnorm_quant_kernel<2>, dim3(rows), dim3(256), 0, stream, x, ldx, w, eps, out, ldo,
+               H, inv_scale, row_scales);
+  else if (nv <= 4)
+    launch_pdl(rmsnorm_quant_kernel<4>, dim3(rows), dim3(256), 0, stream, x, ldx, w, eps, out, ldo,
+               H, inv_scale, row_scales);
+  else
+    throw std::invalid_argument("rmsnorm_quant: H above 8192");
+}
+
+}  // namespace b200

@@ -97,6 +97,11 @@ def build_model(args: EngineArgs, tp: GroupComm = SINGLE):
         model.init_random(seed=args.seed)
     else:
         load_checkpoint_into(model, model_path)
+    fp8_scales = _static_fp8_scales(model_path) if model_path is not None else None
+    if fp8_scales is not None or b200_config.quantization == "fp8_static":
+        if not hasattr(model, "quantize_fp8_static"):
+            raise ValueError(f"{type(model).__name__} does not support static FP8 linears")
+        model.quantize_fp8_static(fp8_scales)
     if args.kv_cache_dtype not in (None, "auto"):
         if not hasattr(model, "set_kv_cache_dtype"):
             raise ValueError(f"{type(model).__name__} does not support kv_cache_dtype={args.kv_cache_dtype!r}")
@@ -110,6 +115,37 @@ def build_model(args: EngineArgs, tp: GroupComm = SINGLE):
 
         model.enable_fused_comm(ps.get_parallel_state().cpu)
     return arch, model, model_path, device, b200_config
+
+
+def _static_fp8_scales(model_path) -> dict | None:
+    """``{(layer, proj): (weight_scale, input_scale)}`` of a static per-tensor FP8 checkpoint
+    (a scalar ``*.weight_scale`` and ``*.input_scale`` per projection, no block scales), else
+    None.  Such checkpoints run W8A8 on the FP8 GEMM; block-scaled ones are dequantized."""
+    import re
+
+    from ..utils.checkpoints import SafetensorsCheckpoint
+
+    try:
+        ck = SafetensorsCheckpoint(model_path)
+    except (FileNotFoundError, OSError, ValueError):
+        return None
+    names = ck.names()
+    if any(n.endswith("_scale_inv") for n in names):
+        return None
+    pat = re.compile(r"layers\.(\d+)\.(?:self_attn|mlp)\.(\w+_proj)\.input_scale$")
+    out = {}
+    for n in names:
+        m = pat.search(n)
+        if not m:
+            continue
+        ws = n[:-len("input_scale")] + "weight_scale"
+        if ws not in names:
+            continue
+        a, b = ck.get(ws), ck.get(n)
+        if a.numel() != 1 or b.numel() != 1:
+            return None  # per-channel / per-token schemes are not the static per-tensor layout
+        out[(int(m.group(1)), m.group(2))] = (float(a.float()), float(b.float()))
+    return out or None
 
 
 def _kv_scales_from_checkpoint(model, model_path) -> list[tuple[float, float]] | None:

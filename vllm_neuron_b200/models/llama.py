@@ -201,7 +201,8 @@ class LlamaForCausalLM(torch.nn.Module):
             # Sequence-parallel prefill with the all-gather / reduce-scatter fused into the GEMMs
             # and the norm: dense SwiGLU decoders without an o_proj bias
             if (self.sequence_parallel and type(self)._mlp is LlamaForCausalLM._mlp
-                    and all(getattr(ly, "o_bias", None) is None for ly in self.layers)):
+                    and all(getattr(ly, "o_bias", None) is None for ly in self.layers)
+                    and not getattr(self, "fp8_linears", 0)):
                 from ..parallel.fused import SPFusedComm
 
                 self.sp_fused = SPFusedComm(self.tp, self.H, self.max_tokens + self.tp.world, self.device,
@@ -233,6 +234,37 @@ class LlamaForCausalLM(torch.nn.Module):
         """Per-tensor (k_scale, v_scale) of an fp8 cache layer (1.0 when not quantized)."""
         sc = getattr(self, "kv_scales", None)
         return sc[kv_layer] if sc else (1.0, 1.0)
+
+    # projections of a decoder layer and the checkpoint names whose scales they take
+    FP8_LINEARS = (("qkv", ("q_proj", "k_proj", "v_proj")), ("o", ("o_proj",)),
+                   ("gate_up", ("gate_proj", "up_proj")), ("down", ("down_proj",)))
+
+    @torch.no_grad()
+    def quantize_fp8_static(self, scales: dict | None = None, default_in_scale: float = 1.0 / 32):
+        """Switch the dense projections to static per-tensor FP8 (W8A8) on the tcgen05 FP8 GEMM.
+        ``scales[(layer, proj)] = (weight_scale, input_scale)`` from the checkpoint; fused
+        projections take the largest scale of their parts (requantized), and without
+        checkpoint scales the weight scale is amax / 448 and the input scale
+        ``default_in_scale``.  Reference: vllm_neuron/model/llama3/quantization.py:39-310."""
+        n = 0
+        for i, ly in enumerate(self.layers):
+            for name, parts in self.FP8_LINEARS:
+                w = getattr(ly, name, None)
+                if w is None or isinstance(w, L.FP8Weight) or not isinstance(w, torch.Tensor):
+                    continue
+                ws = ins = None
+                if scales:
+                    got = [scales[(i, p)] for p in parts if (i, p) in scales]
+                    if got:
+                        ws = max(g[0] for g in got)
+                        ins = max(g[1] for g in got)
+                fw = L.FP8Weight.from_weight(w, ws, ins if ins is not None else default_in_scale)
+                if name in getattr(ly, "_parameters", {}):
+                    del ly._parameters[name]
+                setattr(ly, name, fw)
+                n += 1
+        self.fp8_linears = n
+        return n
 
     def set_kv_cache_dtype(self, kv_cache_dtype: str, scales: list[tuple[float, float]] | None = None):
         """``"auto"`` keeps the model dtype; ``"fp8"`` / ``"fp8_e4m3"`` stores e4m3 K/V with

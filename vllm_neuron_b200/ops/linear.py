@@ -29,6 +29,78 @@ EPI_F32_RED = 2
 EPI_F32_RED_T = 3
 EPI_SILU_BF16 = 4
 
+FP8_MAX = 448.0
+
+
+class FP8Weight:
+    """Static per-tensor FP8 (e4m3) weight ``[N, K]`` of a linear layer, with its weight scale and
+    the static scale of its input activations (W8A8, as in ModelOpt / compressed-tensors static
+    FP8 checkpoints): ``y = (quant(x / in_scale) @ q^T) * in_scale * w_scale``.  The GEMM functions
+    below accept it wherever they take a bf16 weight.  Reference: the ModelOpt static FP8 path,
+    vllm_neuron/model/llama3/quantization.py:39-310."""
+
+    def __init__(self, q: torch.Tensor, w_scale: float, in_scale: float):
+        assert q.dtype == torch.float8_e4m3fn and q.dim() == 2
+        self.q = q
+        self.w_scale = float(w_scale)
+        self.in_scale = float(in_scale)
+
+    @classmethod
+    def from_weight(cls, w: torch.Tensor, w_scale: float | None = None, in_scale: float = 1.0 / 32) -> "FP8Weight":
+        """Quantize ``w`` with ``w_scale`` (default: amax / 448)."""
+        if w_scale is None:
+            w_scale = max(float(w.detach().abs().max()), 1e-12) / FP8_MAX
+        return cls(quantize_fp8(w.detach(), w_scale), w_scale, in_scale)
+
+    @property
+    def shape(self):
+        return self.q.shape
+
+    @property
+    def device(self):
+        return self.q.device
+
+    def dequant(self) -> torch.Tensor:
+        return self.q.float() * self.w_scale
+
+
+def quantize_fp8(x: torch.Tensor, scale: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``satfinite(x / scale)`` as ``torch.float8_e4m3fn`` (the rule of the quant kernels)."""
+    if out is None:
+        out = torch.empty(x.shape, dtype=torch.float8_e4m3fn, device=x.device)
+    inv = 1.0 / float(scale)
+    if x.is_cuda and x.dtype == torch.bfloat16 and x.dim() == 2 and x.stride(1) == 1 and x.shape[1] % 8 == 0:
+        ext().quant_fp8(x, out, inv)
+        return out
+    out.copy_((x.float() * torch.tensor(inv, dtype=torch.float32)).clamp(-FP8_MAX, FP8_MAX).to(torch.float8_e4m3fn))
+    return out
+
+
+def rmsnorm_quant(x: torch.Tensor, w: torch.Tensor, eps: float, scale: float | None = None
+                  ) -> tuple[torch.Tensor, torch.Tensor | None]:
+    """``rmsnorm(x) * w`` quantized to e4m3: with a static per-tensor ``scale`` (STATIC) or, with
+    ``scale=None``, a per-row scale ``max|y| / 448`` returned as fp32 ``[rows]`` (ROW).
+    Reference: vllm_neuron/functional/rmsnorm_quant.py:216."""
+    out = torch.empty(x.shape, dtype=torch.float8_e4m3fn, device=x.device)
+    rows = None if scale is not None else torch.empty(x.shape[0], dtype=torch.float32, device=x.device)
+    if x.is_cuda:
+        ext().rmsnorm_quant(x, w, eps, out, 1.0 / scale if scale is not None else 1.0, rows)
+        return out, rows
+    xf = x.float()
+    y = (xf * torch.rsqrt((xf * xf).mean(-1, keepdim=True) + eps)).to(torch.bfloat16).float() * w.float()
+    if scale is None:
+        rows = (y.abs().amax(-1) / FP8_MAX).clamp_min(1e-30)
+        rows = torch.where(y.abs().amax(-1) > 0, rows, torch.ones_like(rows))
+        out.copy_((y / rows[:, None]).clamp(-FP8_MAX, FP8_MAX).to(torch.float8_e4m3fn))
+    else:
+        out.copy_((y * torch.tensor(1.0 / scale)).clamp(-FP8_MAX, FP8_MAX).to(torch.float8_e4m3fn))
+    return out, rows
+
+
+def _fp8_ref(xq: torch.Tensor, w: FP8Weight) -> torch.Tensor:
+    return (xq.float() @ w.q.float().t()) * (w.in_scale * w.w_scale)
+
+
 SKINNY_MAX = 128
 SILU_BLOCK = 128  # gate/up interleave block = BN/2 of the fused SwiGLU epilogue
 
@@ -62,10 +134,10 @@ def skinny_bn(m: int) -> int:
     raise ValueError(m)
 
 
-def pick_splits(n_rows: int, k: int, sms: int) -> int:
+def pick_splits(n_rows: int, k: int, sms: int, k_block: int = 64) -> int:
     """Split-K factor so that (row tiles x splits) covers the SMs, keeping >= 4 K-blocks."""
     tiles = math.ceil(n_rows / 128)
-    kb = math.ceil(k / 64)
+    kb = math.ceil(k / k_block)
     if tiles >= sms:
         return 1
     s = max(1, min(sms // tiles, kb // 4))
@@ -78,7 +150,15 @@ def gemm_out(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,
     M, K = x.shape
     N = w.shape[0]
     if out is None:
-        out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+        out = torch.empty((M, N), dtype=torch.bfloat16 if x.is_cuda else x.dtype, device=x.device)
+    if isinstance(w, FP8Weight):
+        xq = quantize_fp8(x, w.in_scale)
+        if not x.is_cuda:
+            out.copy_(_fp8_ref(xq, w).to(out.dtype))
+            return out
+        ext().gemm_fp8(xq, w.q, out, EPI_BF16, bn or _pick_bn_wide(M, N, num_sms(x.device)), 1,
+                       w.in_scale * w.w_scale)
+        return out
     if not x.is_cuda:
         out.copy_((x.float() @ w.float().t()).to(out.dtype))
         return out
@@ -92,6 +172,8 @@ def gemm_skinny_bf16(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None 
     """Decode regime without split-K: swapped operands, transposed bf16 store."""
     M, K = x.shape
     N = w.shape[0]
+    if isinstance(w, FP8Weight):  # FP8 keeps the row-major regime (no transposed FP8 store)
+        return gemm_out(x, w, out)
     if out is None:
         out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
     if not x.is_cuda:
@@ -110,6 +192,20 @@ def gemm_accumulate(x: torch.Tensor, w: torch.Tensor, acc: torch.Tensor,
     M, K = x.shape
     N = w.shape[0]
     assert acc.dtype == torch.float32 and acc.shape[0] >= M and acc.shape[1] == N
+    if isinstance(w, FP8Weight):
+        xq = quantize_fp8(x, w.in_scale)
+        if not x.is_cuda:
+            acc[:M].add_(_fp8_ref(xq, w))
+            return acc
+        sms = num_sms(x.device)
+        if M <= SKINNY_MAX:
+            s = splits if splits is not None else pick_splits(N, K, sms, 128)
+            ext().gemm_fp8(w.q, xq, acc, EPI_F32_RED_T, skinny_bn(M), s, w.in_scale * w.w_scale)
+        else:
+            rows = math.ceil(M / 128) * 128 * math.ceil(N / 128)
+            s = splits if splits is not None else pick_splits(rows, K, sms, 128)
+            ext().gemm_fp8(xq, w.q, acc, EPI_F32_RED, 128, s, w.in_scale * w.w_scale)
+        return acc
     if not x.is_cuda:
         acc[:M].add_(x.float() @ w.float().t())
         return acc
@@ -136,6 +232,13 @@ def gemm_silu(x: torch.Tensor, w_gu: torch.Tensor, out: torch.Tensor | None = No
     N2 = w_gu.shape[0]
     if out is None:
         out = torch.empty((M, N2 // 2), dtype=torch.bfloat16, device=x.device)
+    if isinstance(w_gu, FP8Weight):
+        xq = quantize_fp8(x, w_gu.in_scale)
+        if not x.is_cuda:
+            out.copy_(silu_mul_ref(_fp8_ref(xq, w_gu), SILU_BLOCK).to(out.dtype))
+            return out
+        ext().gemm_fp8(xq, w_gu.q, out, EPI_SILU_BF16, 2 * SILU_BLOCK, 1, w_gu.in_scale * w_gu.w_scale)
+        return out
     if not x.is_cuda:
         y = x.float() @ w_gu.float().t()
         out.copy_(silu_mul_ref(y, SILU_BLOCK).to(out.dtype))

@@ -81,7 +81,7 @@ def sample_ref(logits, temperature, top_k, top_p, seeds, offsets, min_p=None) ->
         keep = filter_mask_ref(x, int(top_k[b]), float(top_p[b]),
                                float(min_p[b]) if min_p is not None else 0.0)
         probs = torch.softmax(x.masked_fill(~keep, float("-inf")), -1)
-        g = torch.Generator().manual_seed(int(seeds[b]) * 1000003 + int(offsets[b]))
+        g = torch.Generator().manual_seed((int(seeds[b]) * 1000003 + int(offsets[b])) & 0x7FFFFFFFFFFFFFFF)
         out[b] = int(torch.multinomial(probs, 1, generator=g))
     return out.to(logits.device)
 
