@@ -87,6 +87,35 @@ def bench_gemms(tp: int):
     return rows
 
 
+def bench_gemms_fp8(tp: int):
+    """Static FP8 (W8A8) projections of the Llama-3-8B shapes next to the bf16 kernels: the time
+    includes the activation quantization kernel; bytes count the fp8 weight."""
+    H, I, Hq, Hkv, D = 4096, 14336, 32, 8, 128
+    shapes = {"qkv": ((Hq + 2 * Hkv) * D // tp, H), "o_proj": (H, Hq * D // tp),
+              "gate_up": (2 * I // tp, H), "down": (H, I // tp)}
+    rows = []
+    dev = "cuda"
+    for M in (8192, 64):
+        for name, (N, K) in shapes.items():
+            x = torch.randn(M, K, device=dev, dtype=torch.bfloat16)
+            w = torch.randn(N, K, device=dev, dtype=torch.bfloat16) * 0.02
+            fw = L.FP8Weight.from_weight(w, in_scale=float(x.float().abs().max()) / 448)
+            if M > L.SKINNY_MAX:
+                out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+                fn8 = lambda: L.gemm_out(x, fw, out)
+                fn16 = lambda: L.gemm_out(x, w, out)
+            else:
+                acc = torch.zeros(M, N, device=dev, dtype=torch.float32)
+                fn8 = lambda: L.gemm_accumulate(x, fw, acc)
+                fn16 = lambda: L.gemm_accumulate(x, w, acc)
+            t8, t16 = timeit(fn8), timeit(fn16)
+            rows.append({"op": f"gemm_fp8_{name}", "M": M, "N": N, "K": K, "fp8_ms": t8, "bf16_ms": t16,
+                         "fp8_tflops": 2.0 * M * N * K / t8 / 1e9, "fp8_weight_gbs": N * K / t8 / 1e6,
+                         "speedup_vs_bf16": t16 / t8})
+            print(json.dumps(rows[-1]), flush=True)
+    return rows
+
+
 def bench_decode_attention(tp: int):
     Hq, Hkv, D, bs = 32 // tp, max(1, 8 // tp), 128, 16
     rows = []
@@ -234,6 +263,8 @@ def main():
     only = a.only.split(",")
     if "gemm" in only:
         rows += bench_gemms(a.tp)
+    if "fp8gemm" in only:
+        rows += bench_gemms_fp8(a.tp)
     if "decode" in only:
         rows += bench_decode_attention(a.tp)
     if "prefill" in only:
