@@ -24,11 +24,13 @@ sys.path.insert(0, sys.argv[1])
 from vllm_neuron_b200.entrypoints import LLM
 from vllm_neuron_b200.engine.sampling_params import SamplingParams
 ckpt, out_path, fused, sp = sys.argv[2], sys.argv[3], sys.argv[4] == "1", sys.argv[5] == "1"
+sdp = len(sys.argv) > 6 and sys.argv[6] == "1"
 MAX_TOKENS = [12, 5, 9, 12, 3, 7]  # the decode batch shrinks as requests finish
 torch.cuda.set_device(int(os.environ["LOCAL_RANK"]))
 llm = LLM(ckpt, tensor_parallel_size=int(os.environ["WORLD_SIZE"]), max_num_seqs=8, max_model_len=256,
           num_gpu_blocks=256, max_num_batched_tokens=256, skip_tokenizer_init=True,
-          additional_config={"b200_config": {"fused_comm": fused, "sequence_parallel": sp}})
+          additional_config={"b200_config": {"fused_comm": fused, "sequence_parallel": sp,
+                                             "sampling_dp": sdp}})
 g = torch.Generator().manual_seed(0)
 prompts = [torch.randint(0, 32000, (40,), generator=g).tolist() for _ in range(6)]
 sps = [SamplingParams(temperature=0, max_tokens=n, ignore_eos=True) for n in MAX_TOKENS]
@@ -37,6 +39,7 @@ from vllm_neuron_b200.ops._ext import ext
 torch.cuda.synchronize()
 assert ext().read_status() == 0, "a bounded peer wait expired"
 assert llm.engine.model.sp_forwards > 0 or not sp, "sequence-parallel prefill did not run"
+assert not sdp or llm.engine.runner.sampling_dp_steps > 0, "sampling DP did not run"
 spf = llm.engine.model.sp_fused
 assert not (fused and sp) or (spf is not None and spf.forwards > 0), "fused SP collectives did not run"
 if int(os.environ["RANK"]) == 0:
@@ -69,21 +72,22 @@ def ckpt():
     return d
 
 
-def _run_tp(ckpt, world, fused, sp=False):
+def _run_tp(ckpt, world, fused, sp=False, sdp=False):
     out = tempfile.mktemp(suffix=".json")
     script = tempfile.mktemp(suffix=".py")
     with open(script, "w") as f:
         f.write(WORKER)
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={world}",
-           "--master-addr=127.0.0.1", f"--master-port={_port()}", script, ROOT, ckpt, out, "1" if fused else "0", "1" if sp else "0"]
+           "--master-addr=127.0.0.1", f"--master-port={_port()}", script, ROOT, ckpt, out, "1" if fused else "0", "1" if sp else "0", "1" if sdp else "0"]
     r = subprocess.run(["timeout", "-k", "30", "300"] + cmd, env=env, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     return json.load(open(out))
 
 
-@pytest.mark.parametrize("fused,sp", [(False, False), (True, False), (False, True), (True, True)])
-def test_tp2_matches_tp1(ckpt, fused, sp):
+@pytest.mark.parametrize("fused,sp,sdp", [(False, False, False), (True, False, False), (False, True, False),
+                                          (True, True, False), (True, False, True)])
+def test_tp2_matches_tp1(ckpt, fused, sp, sdp):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     from vllm_neuron_b200.engine.sampling_params import SamplingParams
@@ -95,7 +99,7 @@ def test_tp2_matches_tp1(ckpt, fused, sp):
     ref = LLM(ckpt, max_num_seqs=8, max_model_len=256, num_gpu_blocks=256, max_num_batched_tokens=256,
               skip_tokenizer_init=True).generate(prompts, sps)
     ref = [o.outputs[0].token_ids for o in ref]
-    got = _run_tp(ckpt, 2, fused, sp)
+    got = _run_tp(ckpt, 2, fused, sp, sdp)
     # bf16 reduction order differs between TP sizes: require the first tokens to agree and
     # most of the sequence to match.
     same = sum(a == b for r, g2 in zip(ref, got) for a, b in zip(r, g2))

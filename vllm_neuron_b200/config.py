@@ -190,6 +190,7 @@ class B200Config:
     cuda_graphs: bool = True
     fused_comm: bool = True           # fused GEMM+collective kernels (else NCCL baseline)
     use_cublas_baseline: bool = False  # library GEMMs instead of the tcgen05 kernels
+    sampling_dp: bool = False          # TP decode: each rank samples 1/W of the rows (all-to-all)
     extra: dict = field(default_factory=dict)
 
     @classmethod

@@ -195,6 +195,7 @@ class LLMEngine:
         max_tok = max(args.max_num_batched_tokens, args.max_num_seqs)
         real_group = tp.world > 1 and tp.group is not None
         self.runner = build_runner(args, self.model, self.max_model_len, self.device, self.b200_config)
+        self.runner.sampling_dp = bool(self.b200_config.sampling_dp)
         nb = args.num_gpu_blocks or self.runner.profile_num_blocks(args.gpu_memory_utilization)
         if real_group and self.device.type == "cuda":
             t = torch.tensor([nb], dtype=torch.int64, device=self.device)

@@ -507,6 +507,8 @@ class LlamaForCausalLM(torch.nn.Module):
             L.gemm_skinny_bf16(xs, self.lm_head, out=logits)
         else:
             L.gemm_out(xs, self.lm_head, out=logits)
+        if getattr(self, "skip_logits_gather", False):
+            return logits  # vocab shard [S, V_local] (sampling data parallelism)
         if self.tp.world > 1:
             logits = self.tp.all_gather(logits, dim=1)
         return logits[:, : self.V]

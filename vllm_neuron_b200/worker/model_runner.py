@@ -60,6 +60,8 @@ class ModelRunner:
                  block_size: int = 16, cuda_graphs: bool = True, graph_buckets: list[int] | None = None,
                  device="cuda", seed: int = 0):
         self.model = model
+        self.sampling_dp = False   # sampling data parallelism over the TP group (see _sample_dp)
+        self.sampling_dp_steps = 0
         self.device = torch.device(device)
         self.is_cuda = self.device.type == "cuda"
         self.max_num_seqs = max_num_seqs
@@ -360,6 +362,9 @@ class ModelRunner:
 
     def _forward_and_sample(self, fb: ForwardBatch, samp: dict, S: int, tok_out: torch.Tensor,
                             lp_out: torch.Tensor | None, bitmask: torch.Tensor | None = None):
+        tp = getattr(self.model, "tp", None)
+        if self.sampling_dp and bitmask is None and tp is not None and tp.world > 1 and tp.group is not None:
+            return self._sample_dp(fb, samp, S, tok_out, lp_out)
         logits = self.model.forward(fb)
         if bitmask is not None:
             ops.sampling.apply_token_bitmask(logits, bitmask)
@@ -367,6 +372,50 @@ class ModelRunner:
                    samp["offsets"], min_p=samp["min_p"], out=tok_out[:S],
                    out_logprob=lp_out[:S] if lp_out is not None else None,
                    row_slots=samp["row_slots"], last_tok=self.last_tok)
+
+    def _sample_dp(self, fb: ForwardBatch, samp: dict, S: int, tok_out: torch.Tensor,
+                   lp_out: torch.Tensor | None):
+        """Sampling data parallelism over the TP group: the LM head's vocab-sharded logits
+        ``[S, V/W]`` are exchanged by one all-to-all into ``[S/W, V]`` row blocks, each rank
+        samples its rows, and the tokens (and logprobs) are all-gathered.  Rows sample with
+        their own seeds, so the tokens equal the replicated path's.  Reference: sampling DP,
+        the sampling all-to-all / gather groups (vllm_neuron/parallel/neuron_parallel_state.py:
+        116-133,546-574; functional/topk.py:222-322)."""
+        import torch.distributed as dist
+
+        m = self.model
+        tp = m.tp
+        W, r = tp.world, tp.rank
+        m.skip_logits_gather = True
+        try:
+            local = m.forward(fb)                                 # [S, V_local]
+        finally:
+            m.skip_logits_gather = False
+        Vl = local.shape[1]
+        per = -(-S // W)
+        send = torch.zeros(W * per, Vl, dtype=local.dtype, device=local.device)
+        send[:S] = local[:S]
+        recv = torch.empty_like(send)
+        dist.all_to_all_single(recv, send, group=tp.group)        # block w: rows of rank r, vocab shard w
+        mine = recv.view(W, per, Vl).permute(1, 0, 2).reshape(per, W * Vl)[:, :m.V]
+
+        def rows(t):
+            p = torch.zeros(W * per, dtype=t.dtype, device=t.device)
+            p[:S] = t[:S]
+            return p[r * per:(r + 1) * per]
+
+        mp = {k: rows(samp[k]) for k in ("temperature", "top_k", "top_p", "min_p", "offsets")}
+        seeds = torch.zeros(W * per, dtype=samp["seeds"].dtype, device=samp["seeds"].device)
+        seeds[:S] = samp["seeds"][:S]
+        tok = torch.empty(per, dtype=torch.int32, device=local.device)
+        lp = torch.empty(per, dtype=torch.float32, device=local.device) if lp_out is not None else None
+        ops.sample(mine, mp["temperature"], mp["top_k"], mp["top_p"], seeds[r * per:(r + 1) * per],
+                   mp["offsets"], min_p=mp["min_p"], out=tok, out_logprob=lp)
+        tok_out[:S].copy_(tp.all_gather(tok, dim=0)[:S])
+        if lp_out is not None:
+            lp_out[:S].copy_(tp.all_gather(lp, dim=0)[:S])
+        self.last_tok[samp["row_slots"][:S].long()] = tok_out[:S]
+        self.sampling_dp_steps += 1
 
     # ------------------------------------------------------------------ graphs
     def capture_graphs(self):
