@@ -77,6 +77,9 @@ def main():
     ap.add_argument("--max-num-batched-tokens", type=int, default=8192)
     ap.add_argument("--warmup-prompts", type=int, default=4)
     ap.add_argument("--json", default=None)
+    ap.add_argument("--quant", default=None, choices=[None, "fp8_static"],
+                    help="fp8_static: W8A8 FP8 projections (random weights quantized per tensor)")
+    ap.add_argument("--sp", action="store_true", help="sequence-parallel prefill (TP > 1)")
     a = ap.parse_args()
 
     from vllm_neuron_b200.engine.sampling_params import SamplingParams
@@ -93,9 +96,14 @@ def main():
     OUT = a.output_len or OUT
     max_len = IN + OUT + 16
     blocks = P * ((max_len + 15) // 16) + 64
+    nc = {}
+    if a.quant:
+        nc["quantization"] = a.quant
+    if a.sp:
+        nc["sequence_parallel"] = True
     llm = LLM(dict(m["cfg"]), tensor_parallel_size=world, max_num_seqs=P, max_model_len=max_len,
               max_num_batched_tokens=a.max_num_batched_tokens, load_format="dummy", num_gpu_blocks=blocks,
-              skip_tokenizer_init=True, seed=0)
+              skip_tokenizer_init=True, seed=0, additional_config={"neuron_config": nc} if nc else None)
     vocab = m["cfg"]["vocab_size"]
     g = torch.Generator().manual_seed(7)
     prompts = torch.randint(0, vocab, (P, IN), generator=g).tolist()
@@ -124,7 +132,8 @@ def main():
     res = {"model": a.model, "tp": world, "num_prompts": P, "input_len": IN, "output_len": OUT,
            "output_tok_s": P * OUT / (ms / 1e3), "wall_s": wall, "device_s": ms / 1e3,
            "p50_ttft_ms": float(np.median(ttft)) * 1e3, "p50_tpot_ms": float(np.median(tpot)) * 1e3,
-           "dtype": "bf16", "data": "synthetic prompts, random-init weights"}
+           "dtype": "bf16" + (" activations, fp8 W8A8 projections" if a.quant else ""),
+           "sp": bool(a.sp), "data": "synthetic prompts, random-init weights"}
     if rank == 0:
         print(json.dumps(res), flush=True)
         if a.json:
