@@ -501,8 +501,9 @@ constexpr int kGdnCols = 32;
 constexpr int kSS = 36;        // fp32 row stride of S / Delta (conflict-free B fragments)
 constexpr int kWStride = 132;  // fp32 row stride of W (conflict-free A fragments)
 constexpr int kQStride = 136;  // bf16 row stride of q and k
+constexpr int kQKStride = 72;  // bf16 row stride of the staged masked Q^K^T block
 constexpr int kGdnStateSmem = 128 * kSS * 4 + kGC * kWStride * 4 + 2 * kGC * kQStride * 2 +
-                              kGC * kSS * 4 + 4 * kGC * 4;
+                              kGC * kSS * 4 + 4 * kGC * 4 + kGC * kQKStride * 2;
 
 namespace {
 __device__ __forceinline__ uint32_t tf32(float x) {
@@ -547,6 +548,8 @@ __global__ void __launch_bounds__(256) gdn_chunk_state_kernel(const GatedDeltaPa
   float* sqf = slg + kGC;        // [64] gamma_t |q|^-1 dk^-1/2
   float* skf = sqf + kGC;        // [64] |k|^-1 e^{lg_L - lg_t}
   float* sik = skf + kGC;        // [64] |k|^-1
+  // decay-masked Q^K^T of the chunk, bf16 (it only feeds the bf16 output, not the state)
+  __nv_bfloat16* sQK = reinterpret_cast<__nv_bfloat16*>(sik + kGC);  // [64][72]
   float* S = p.state + (long long)bt.slots[b] * p.state_slot_stride + (long long)h * 128 * 128 +
              cg * kGdnCols;
   for (int i = tid; i < 128 * kGdnCols / 4; i += 256) {
@@ -580,6 +583,15 @@ __global__ void __launch_bounds__(256) gdn_chunk_state_kernel(const GatedDeltaPa
       *reinterpret_cast<uint4*>(sQ + r * kQStride + c8 * 8) = qv;
       *reinterpret_cast<uint4*>(sK + r * kQStride + c8 * 8) = kv;
     }
+    {
+      const float* qk = cs.QKm + ((long long)c * p.Hv + h) * (kGC * kGC);
+      for (int i = tid; i < kGC * kGC / 4; i += 256) {  // rows past L are zero in QKm
+        const int r = i >> 4, c4 = i & 15;
+        const float4 v = *reinterpret_cast<const float4*>(qk + r * kGC + c4 * 4);
+        *reinterpret_cast<uint2*>(sQK + r * kQKStride + c4 * 4) =
+            make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+      }
+    }
     if (tid < kGC) {
       float lg = 0.f, qf = 0.f, ik = 0.f;
       if (tid < L) {
@@ -602,6 +614,14 @@ __global__ void __launch_bounds__(256) gdn_chunk_state_kernel(const GatedDeltaPa
       float acc[2][4];
 #pragma unroll
       for (int j = 0; j < 2; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+      float2 uu[2][2];  // U loads issued before the product so their latency overlaps it
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int col = nh * 16 + j * 8 + 2 * t4;
+        uu[j][0] = uu[j][1] = make_float2(0.f, 0.f);
+        if (r0 < L) uu[j][0] = *reinterpret_cast<const float2*>(cs.U + ((long long)(t0 + r0) * p.Hv + h) * 128 + cg * kGdnCols + col);
+        if (r1 < L) uu[j][1] = *reinterpret_cast<const float2*>(cs.U + ((long long)(t0 + r1) * p.Hv + h) * 128 + cg * kGdnCols + col);
+      }
 #pragma unroll 2
       for (int ks = 0; ks < 16; ++ks) {
         const int kc = ks * 8 + t4;
@@ -624,9 +644,7 @@ __global__ void __launch_bounds__(256) gdn_chunk_state_kernel(const GatedDeltaPa
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
         const int col = nh * 16 + j * 8 + 2 * t4;
-        float2 u0 = make_float2(0.f, 0.f), u1 = u0;
-        if (r0 < L) u0 = *reinterpret_cast<const float2*>(cs.U + ((long long)(t0 + r0) * p.Hv + h) * 128 + cg * kGdnCols + col);
-        if (r1 < L) u1 = *reinterpret_cast<const float2*>(cs.U + ((long long)(t0 + r1) * p.Hv + h) * 128 + cg * kGdnCols + col);
+        const float2 u0 = uu[j][0], u1 = uu[j][1];
         *reinterpret_cast<float2*>(sD + r0 * kSS + col) = make_float2(u0.x - acc[j][0], u0.y - acc[j][1]);
         *reinterpret_cast<float2*>(sD + r1 * kSS + col) = make_float2(u1.x - acc[j][2], u1.y - acc[j][3]);
       }
@@ -654,11 +672,10 @@ __global__ void __launch_bounds__(256) gdn_chunk_state_kernel(const GatedDeltaPa
         acc[j][0] *= f0; acc[j][1] *= f0; acc[j][2] *= f1; acc[j][3] *= f1;
       }
       // QKm is lower triangular: k steps past this m tile's last row contribute nothing
-      const float* qk = cs.QKm + ((long long)c * p.Hv + h) * (kGC * kGC);
       for (int ks = 0; ks < 2 * mt + 2; ++ks) {
         const int kc = ks * 8 + t4;
-        const uint32_t a0 = tf32(__ldg(qk + r0 * kGC + kc)), a1 = tf32(__ldg(qk + r1 * kGC + kc));
-        const uint32_t a2 = tf32(__ldg(qk + r0 * kGC + kc + 4)), a3 = tf32(__ldg(qk + r1 * kGC + kc + 4));
+        const uint32_t a0 = tf32(bf(sQK + r0 * kQKStride + kc)), a1 = tf32(bf(sQK + r1 * kQKStride + kc));
+        const uint32_t a2 = tf32(bf(sQK + r0 * kQKStride + kc + 4)), a3 = tf32(bf(sQK + r1 * kQKStride + kc + 4));
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
           const int col = nh * 16 + j * 8 + g;
