@@ -11,6 +11,7 @@ from vllm_neuron_b200.engine.sampling_params import SamplingParams
 from vllm_neuron_b200.entrypoints import LLM
 
 IMG, VS, VE = 500, 501, 502  # image pad, vision start, vision end token ids
+VID = 503                      # video pad
 PROC = {"min_pixels": 16 * 16, "max_pixels": 32 * 32}
 
 
@@ -28,7 +29,8 @@ def _ckpt():
                            temporal_patch_size=2, spatial_merge_size=2, out_hidden_size=64,
                            num_position_embeddings=16, deepstack_visual_indexes=[0, 1],
                            initializer_range=0.05),
-        image_token_id=IMG, vision_start_token_id=VS, vision_end_token_id=VE, tie_word_embeddings=False)
+        image_token_id=IMG, video_token_id=VID, vision_start_token_id=VS, vision_end_token_id=VE,
+        tie_word_embeddings=False)
     hf = Qwen3VLForConditionalGeneration(cfg).float().eval()
     with torch.no_grad():
         for n, p in hf.model.visual.named_parameters():
@@ -97,3 +99,43 @@ def test_mrope_positions_layout():
     assert pos[2, 2:8].tolist() == [2, 3, 4, 2, 3, 4]
     assert pos[:, 8].tolist() == [5, 5, 5]  # after the image: start + max(h, w) / merge
     assert delta == 6 - 9
+
+
+def test_qwen3_vl_video_matches_hf():
+    """A 4-frame video (two temporal patch groups, each a timestamp + vision span) next to an
+    image: greedy tokens match HF's forward with pixel_values_videos / video_grid_thw."""
+    from vllm_neuron_b200.engine.multimodal import _processor, _video_processor
+
+    d, hf = _ckpt()
+    rng = np.random.default_rng(3)
+    frames = (rng.random((4, 16, 24, 3)) * 255).astype(np.uint8)
+    img = (rng.random((16, 16, 3)) * 255).astype(np.uint8)
+    llm = LLM(d, device="cpu", dtype="float32", max_num_seqs=2, max_model_len=256, num_gpu_blocks=64,
+              max_num_batched_tokens=16, mm_processor_kwargs=PROC, skip_tokenizer_init=True)
+    vc = llm.engine.model.cfg.raw["vision_config"]
+    vo = _video_processor(d, vc, PROC)(videos=[frames], return_tensors="pt", do_sample_frames=False,
+                                       video_metadata=[{"fps": 2.0, "total_num_frames": 4}])
+    t, h, w = vo["video_grid_thw"][0].tolist()
+    n = h * w // 4
+    io = _processor(d, vc, PROC)(images=[img], return_tensors="pt")
+    n_img = int(io["image_grid_thw"].prod()) // 4
+    ts = [90, 91]  # stand-ins for the timestamp text tokens of the two groups
+    ids = [7, VS] + [IMG] * n_img + [VE, 8]
+    for g in range(t):
+        ids += [ts[g], VS] + [VID] * n + [VE]
+    ids += [9, 10]
+    out = llm.generate([{"prompt_token_ids": ids, "multi_modal_data": {"image": img, "video": frames}}],
+                       SamplingParams(temperature=0, max_tokens=5, ignore_eos=True))
+    got = out[0].outputs[0].token_ids
+    ref, cur = [], list(ids)
+    with torch.no_grad():
+        for _ in range(5):
+            x = torch.tensor([cur])
+            mm = (x == IMG).int() + 2 * (x == VID).int()
+            logits = hf(input_ids=x, pixel_values=io["pixel_values"], image_grid_thw=io["image_grid_thw"],
+                        pixel_values_videos=vo["pixel_values_videos"], video_grid_thw=vo["video_grid_thw"],
+                        mm_token_type_ids=mm).logits
+            nxt = int(logits[0, -1].argmax())
+            ref.append(nxt)
+            cur.append(nxt)
+    assert got == ref, (got, ref)

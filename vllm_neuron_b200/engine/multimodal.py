@@ -51,6 +51,82 @@ def _processor(model_dir: str | None, vc: dict, overrides: dict | None):
     return Qwen2VLImageProcessor(**kw)
 
 
+def _video_processor(model_dir: str | None, vc: dict, overrides: dict | None):
+    from transformers.models.qwen3_vl.video_processing_qwen3_vl import Qwen3VLVideoProcessor
+
+    ip = _processor(model_dir, vc, overrides)  # same geometry and normalisation as images
+    return Qwen3VLVideoProcessor(patch_size=ip.patch_size, temporal_patch_size=ip.temporal_patch_size,
+                                 merge_size=ip.merge_size, size=dict(ip.size), image_mean=list(ip.image_mean),
+                                 image_std=list(ip.image_std))
+
+
+def prepare_video_request(prompt: list[int], video, model, model_dir: str | None = None,
+                          processor_kwargs: dict | None = None, fps: float = 2.0,
+                          images=None) -> tuple[list[int], MultiModalInputs]:
+    """Video (frames ``[T, H, W, 3]``) of a Qwen3-VL request, optionally with images.  Qwen3-VL
+    separates a video's temporal patch groups by timestamp text (``<t seconds> <vision_start>
+    <video_pad> ... <vision_end>`` per group), so each group is one vision span with grid
+    (1, h, w): the prompt must already hold those spans (the HF processor's layout; ``video_pad``
+    repeated h w / merge^2 times per group).  Images and video spans are matched to the prompt in
+    order of appearance.  Reference: Qwen3-VL video inputs
+    (vllm_neuron/model/qwen3_vl/utils/vision_preprocessing.py)."""
+    from ..models.qwen3_vl import mrope_positions
+
+    vc = model.cfg.raw.get("vision_config") or {}
+    vp = _video_processor(model_dir, vc, processor_kwargs)
+    frames = np.asarray(video)
+    out = vp(videos=[frames], return_tensors="pt", do_sample_frames=False,
+             video_metadata=[{"fps": fps, "total_num_frames": int(frames.shape[0])}])
+    vpix = out["pixel_values_videos"]
+    t, h, w = (int(v) for v in out["video_grid_thw"][0].tolist())
+    vgrids = [(1, h, w)] * t
+    ipix, igrids = None, []
+    if images is not None:
+        if not isinstance(images, (list, tuple)):
+            images = [images]
+        o = _processor(model_dir, vc, processor_kwargs)(images=list(images), return_tensors="pt")
+        ipix = o["pixel_values"]
+        igrids = [tuple(int(v) for v in g) for g in o["image_grid_thw"].tolist()]
+    m = model.spatial_merge
+    img, vid = model.image_token_id, model.video_token_id
+    # order the vision spans as they appear in the prompt
+    grids, parts = [], []
+    ii = vi = 0
+    ioff = voff = 0
+    i = 0
+    ids = list(prompt)
+    while i < len(ids):
+        x = ids[i]
+        if x == img or x == vid:
+            gl = igrids if x == img else vgrids
+            k = ii if x == img else vi
+            if k >= len(gl):
+                raise ValueError("more vision spans in the prompt than images / video groups")
+            gt, gh, gw = gl[k]
+            n = gt * gh * gw // (m * m)
+            npatch = gt * gh * gw
+            if x == img:
+                parts.append(ipix[ioff:ioff + npatch])
+                ioff += npatch
+                ii += 1
+            else:
+                parts.append(vpix[voff:voff + npatch])
+                voff += npatch
+                vi += 1
+            grids.append((gt, gh, gw))
+            i += n
+        else:
+            i += 1
+    if vi != len(vgrids) or ii != len(igrids):
+        raise ValueError(f"prompt holds {vi} of {len(vgrids)} video groups and {ii} of {len(igrids)} images "
+                         "(spans must be expanded: video_pad x h w / merge^2 per temporal group)")
+    pos3, delta = mrope_positions(ids, {img, vid}, grids, m)
+    rows = np.array([j for j, x in enumerate(ids) if x == img or x == vid], dtype=np.int64)
+    mm = MultiModalInputs(pixels=torch.cat(parts), grids=grids, positions3=pos3, delta=delta, image_rows=rows)
+    mm.row_of = {int(r): j for j, r in enumerate(rows)}
+    return ids, mm
+
+
 def prepare_image_request(prompt: list[int], images, model, model_dir: str | None = None,
                           processor_kwargs: dict | None = None) -> tuple[list[int], MultiModalInputs]:
     """Expand the image placeholders of ``prompt`` and build its MultiModalInputs."""

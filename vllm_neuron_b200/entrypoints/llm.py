@@ -219,8 +219,15 @@ class LLM:
 
                 toks = _normalize_prompt(p, self.tokenizer)
                 images = p["multi_modal_data"].get("image")
-                toks, mm = prepare_image_request(toks, images, self.engine.model, self.engine.model_path,
-                                                 self.mm_processor_kwargs)
+                if p["multi_modal_data"].get("video") is not None:
+                    from ..engine.multimodal import prepare_video_request
+
+                    toks, mm = prepare_video_request(toks, p["multi_modal_data"]["video"], self.engine.model,
+                                                     self.engine.model_path, self.mm_processor_kwargs,
+                                                     fps=float(p.get("fps", 2.0)), images=images)
+                else:
+                    toks, mm = prepare_image_request(toks, images, self.engine.model, self.engine.model_path,
+                                                     self.mm_processor_kwargs)
                 if self._ec is not None and self._ec[0].ec_role == "ec_consumer":
                     self._install_remote_encoding(mm)
                 ids.append(self.engine.add_request(toks, sp, request_id=f"gen-{base}-{i}", mm=mm))

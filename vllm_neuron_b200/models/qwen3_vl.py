@@ -182,19 +182,20 @@ class Qwen3VLVision(torch.nn.Module):
         return emb, deep_t
 
 
-def mrope_positions(prompt: list[int], image_token_id: int, grids: list[tuple[int, int, int]],
+def mrope_positions(prompt: list[int], image_token_id, grids: list[tuple[int, int, int]],
                     merge: int) -> tuple[np.ndarray, int]:
     """3-D positions ``[3, P]`` of a prompt whose image placeholders are already expanded, and
     the position delta of the tokens after the prompt (``pos = index + delta``).  Text tokens
     count up by one; an image of grid (t, h, w) occupies (t h w) / merge^2 tokens at
     (start, start + row, start + col) and advances the counter by max(h, w) / merge."""
+    vis = set(image_token_id) if isinstance(image_token_id, (set, list, tuple)) else {image_token_id}
     P = len(prompt)
     pos = np.zeros((3, P), dtype=np.int64)
     cur = 0
     i = 0
     g = iter(grids)
     while i < P:
-        if prompt[i] != image_token_id:
+        if prompt[i] not in vis:
             pos[:, i] = cur
             cur += 1
             i += 1
@@ -202,7 +203,7 @@ def mrope_positions(prompt: list[int], image_token_id: int, grids: list[tuple[in
         t, h, w = next(g)
         gh, gw = h // merge, w // merge
         n = t * gh * gw
-        if prompt[i:i + n] != [image_token_id] * n:
+        if prompt[i:i + n] != [prompt[i]] * n:
             raise ValueError("image placeholder count does not match the image grid")
         pos[0, i:i + n] = cur
         pos[1, i:i + n] = cur + np.repeat(np.arange(gh), gw * t)
@@ -226,6 +227,7 @@ class Qwen3VLForConditionalGeneration(LlamaForCausalLM):
         sec = rp.get("mrope_section") or [24, 20, 20]
         self.mrope_section = (int(sec[0]), int(sec[1]), int(sec[2]))
         self.image_token_id = int(raw.get("image_token_id", 151655))
+        self.video_token_id = int(raw.get("video_token_id", 151656))
         self.spatial_merge = self.visual.merge
 
     @torch.no_grad()
