@@ -139,3 +139,25 @@ def test_qwen3_vl_video_matches_hf():
             ref.append(nxt)
             cur.append(nxt)
     assert got == ref, (got, ref)
+
+
+def test_encoder_cache_reuses_identical_images():
+    """Two requests with the same image run the vision encoder once (content-hash cache)."""
+    d, _ = _ckpt()
+    rng = np.random.default_rng(4)
+    img = (rng.random((24, 16, 3)) * 255).astype(np.uint8)
+    llm = LLM(d, device="cpu", dtype="float32", max_num_seqs=2, max_model_len=256, num_gpu_blocks=64,
+              max_num_batched_tokens=64, mm_processor_kwargs=PROC, skip_tokenizer_init=True)
+    calls = []
+    vis = llm.engine.model.visual
+    orig = vis.forward
+    vis.forward = lambda *a, **k: (calls.append(1), orig(*a, **k))[1]
+    reqs = [{"prompt_token_ids": [7, 8, VS, IMG, VE, 9], "multi_modal_data": {"image": img}},
+            {"prompt_token_ids": [3, VS, IMG, VE, 4, 5], "multi_modal_data": {"image": img}}]
+    a = llm.generate(reqs, SamplingParams(temperature=0, max_tokens=3, ignore_eos=True))
+    assert len(calls) == 1 and llm.engine.runner.encoder_cache_hits == 1
+    b = LLM(d, device="cpu", dtype="float32", max_num_seqs=2, max_model_len=256, num_gpu_blocks=64,
+            max_num_batched_tokens=64, mm_processor_kwargs=PROC,
+            skip_tokenizer_init=True).generate(reqs[1:], SamplingParams(temperature=0, max_tokens=3,
+                                                                        ignore_eos=True))
+    assert a[1].outputs[0].token_ids == b[0].outputs[0].token_ids

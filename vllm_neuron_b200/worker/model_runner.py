@@ -61,6 +61,7 @@ class ModelRunner:
                  device="cuda", seed: int = 0):
         self.model = model
         self.sampling_dp = False   # sampling data parallelism over the TP group (see _sample_dp)
+        self.encoder_cache_size = 32  # vision encodings kept for reuse (see _encode_cached)
         self.sampling_dp_steps = 0
         self.device = torch.device(device)
         self.is_cuda = self.device.type == "cuda"
@@ -285,7 +286,7 @@ class ModelRunner:
                 if len(sel):
                     need3 = True
                     if mm.emb is None:
-                        mm.emb, mm.deep = self.model.encode_images(mm.pixels.to(self.device), mm.grids)
+                        mm.emb, mm.deep = self._encode_cached(mm)
                     idx = torch.as_tensor([mm.row_of[int(r)] for r in sel], device=mm.emb.device)
                     brows = [t + int(r) - sr.start for r in sel]
                     rows.extend(brows)
@@ -459,6 +460,30 @@ class ModelRunner:
             self.graph_kernels[b] = ops._ext.ext().launch_count() - n0
             torch.cuda.synchronize(self.device)
             self.graphs[b] = (g, lay, buf, tok, lp, w.num_splits)
+
+    def _encode_cached(self, mm):
+        """Vision encoder output of a request, reused across requests with the same pixels and
+        grids (key: content hash) from a bounded LRU cache on the device.  Reference:
+        EncoderCacheBlocks (vllm_neuron/vllm/worker/encoder_cache_blocks.py:45-448, slots keyed by
+        mm_hash)."""
+        import hashlib
+        from collections import OrderedDict
+
+        if not hasattr(self, "encoder_cache"):
+            self.encoder_cache = OrderedDict()
+            self.encoder_cache_hits = 0
+        key = hashlib.sha1(mm.pixels.float().contiguous().numpy().tobytes()
+                           + repr(mm.grids).encode()).hexdigest()
+        hit = self.encoder_cache.get(key)
+        if hit is not None:
+            self.encoder_cache.move_to_end(key)
+            self.encoder_cache_hits += 1
+            return hit
+        out = self.model.encode_images(mm.pixels.to(self.device), mm.grids)
+        self.encoder_cache[key] = out
+        while len(self.encoder_cache) > self.encoder_cache_size:
+            self.encoder_cache.popitem(last=False)
+        return out
 
     def dummy_forward(self):
         """A one-token forward on the null block that writes no KV and samples nothing: an idle
