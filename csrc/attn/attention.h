@@ -36,6 +36,10 @@ struct PagedAttnParams {
   // (applied to the normalized output here).
   int kv_fp8;
   float v_scale;
+  // Decode (TMA kernel and combine): when set, the split factor actually used, read on the
+  // device (1 <= *splits_dev <= num_splits).  Lets a captured CUDA graph (whose num_splits is
+  // sized for max_model_len) split each step by its real context lengths.
+  const int* splits_dev;
 };
 
 void paged_attention_launch(const PagedAttnParams& p, int num_work, int head_dim, bool decode,

@@ -459,9 +459,13 @@ __global__ void attn_combine_kernel(const float* __restrict__ part_o,
 template <int D>
 __global__ void __launch_bounds__(256) attn_combine_warp_kernel(
     const float* __restrict__ part_o, const float* __restrict__ part_lse, __nv_bfloat16* out,
-    long long o_stride_t, int total_tokens, int Hq, int num_splits) {
+    long long o_stride_t, int total_tokens, int Hq, int num_splits, const int* splits_dev) {
   pdl_trigger();
   pdl_wait();
+  if (splits_dev != nullptr) {
+    num_splits = max(1, min(*splits_dev, num_splits));
+    if (num_splits == 1) return;  // the decode kernel wrote the output directly
+  }
   constexpr int PER = D / 32;
   const int wid = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -516,10 +520,14 @@ static void launch_attn(const PagedAttnParams& p, int num_work, cudaStream_t str
     launch_attn_t<D, DECODE, false>(p, num_work, stream);
 }
 
-void paged_attention_launch(const PagedAttnParams& p, int num_work, int head_dim, bool decode,
+void paged_attention_launch(const PagedAttnParams& p_in, int num_work, int head_dim, bool decode,
                             cudaStream_t stream) {
   if (num_work == 0) return;
-  if (decode && paged_decode_tma_supported(p, head_dim)) {
+  PagedAttnParams p = p_in;
+  const bool tma = decode && paged_decode_tma_supported(p, head_dim);
+  // device split factors are a feature of the TMA decode path with the warp combine (<= 32)
+  if (!tma || p.num_splits > 32) p.splits_dev = nullptr;
+  if (tma) {
     paged_decode_tma_launch(p, num_work, head_dim, stream);
   } else if (head_dim == 128) {
     decode ? launch_attn<128, true>(p, num_work, stream)
@@ -539,13 +547,13 @@ void paged_attention_launch(const PagedAttnParams& p, int num_work, int head_dim
     const float* pl = p.part_lse;
     if (head_dim == 128)
       launch_pdl(attn_combine_warp_kernel<128>, grid, dim3(256), 0, stream, po, pl, p.out,
-                 p.o_stride_t, p.total_tokens, p.Hq, p.num_splits);
+                 p.o_stride_t, p.total_tokens, p.Hq, p.num_splits, p.splits_dev);
     else if (head_dim == 256)
       launch_pdl(attn_combine_warp_kernel<256>, grid, dim3(256), 0, stream, po, pl, p.out,
-                 p.o_stride_t, p.total_tokens, p.Hq, p.num_splits);
+                 p.o_stride_t, p.total_tokens, p.Hq, p.num_splits, p.splits_dev);
     else
       launch_pdl(attn_combine_warp_kernel<64>, grid, dim3(256), 0, stream, po, pl, p.out,
-                 p.o_stride_t, p.total_tokens, p.Hq, p.num_splits);
+                 p.o_stride_t, p.total_tokens, p.Hq, p.num_splits, p.splits_dev);
   } else if (p.num_splits > 1) {
     dim3 grid(p.total_tokens, p.Hq);
     if (head_dim == 128)

@@ -102,13 +102,13 @@ struct Unit {
   int s_lo, s_hi;  // tile range [s_lo, s_hi) of 16-token tiles
 };
 
-__device__ __forceinline__ Unit unit_info(const PagedAttnParams& p, int u) {
+__device__ __forceinline__ Unit unit_info(const PagedAttnParams& p, int u, int ns) {
   Unit x;
-  const int per_item = p.Hkv * p.num_splits;
+  const int per_item = p.Hkv * ns;
   const int item = u / per_item;
   const int rem = u - item * per_item;
-  x.kvh = rem / p.num_splits;
-  x.split = rem - x.kvh * p.num_splits;
+  x.kvh = rem / ns;
+  x.split = rem - x.kvh * ns;
   const int2 w = p.work[item];
   x.b = w.x;
   x.row0 = w.y;
@@ -124,7 +124,7 @@ __device__ __forceinline__ Unit unit_info(const PagedAttnParams& p, int u) {
   const int hi = min(x.p_max + 1, x.kv_len);
   const int t_lo = lo / kTok;
   const int t_hi = hi > lo ? (hi + kTok - 1) / kTok : t_lo;
-  const int per = (t_hi - t_lo + p.num_splits - 1) / p.num_splits;
+  const int per = (t_hi - t_lo + ns - 1) / ns;
   x.s_lo = t_lo + x.split * per;
   x.s_hi = min(x.s_lo + per, t_hi);
   return x;
@@ -136,7 +136,7 @@ template <int D, int STAGES, int kWarps, bool FP8>
 __global__ void __launch_bounds__(kWarps * 32, 1)
     paged_decode_kernel(const __grid_constant__ CUtensorMap tk,
                         const __grid_constant__ CUtensorMap tv, const PagedAttnParams p,
-                        int num_units) {
+                        int num_units_max) {
   constexpr int BOXC = FP8 ? (D < 128 ? D : 128) : 64;  // columns per TMA box
   constexpr int BOX_BYTES = kTok * (FP8 ? BOXC : 128);
   constexpr int HALVES = D / BOXC;
@@ -170,6 +170,9 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
 
   uint32_t* status = p.status;
   int* sched = p.sched;
+  // split factor of this step (device value under CUDA graphs, else the launch's)
+  const int ns = p.splits_dev != nullptr ? max(1, min(*p.splits_dev, p.num_splits)) : p.num_splits;
+  const int num_units = num_units_max / p.num_splits * ns;
   uint64_t policy = 0;
   if (lane == 0) policy = policy_evict_first();  // each K/V byte is read once per step
 
@@ -209,10 +212,10 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
         p_done = true;
         return;
       }
-      const Unit x = unit_info(p, u);
+      const Unit x = unit_info(p, u, ns);
       if (x.s_lo >= x.s_hi) {
         // empty split: its partial carries no weight in the combine
-        if (p.num_splits > 1 && lane < x.rows_here) {
+        if (ns > 1 && lane < x.rows_here) {
           const int pr = x.row0 + lane;
           const int tok = x.q_begin + pr / p.G;
           const int head = x.kvh * p.G + pr % p.G;
@@ -242,7 +245,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
   while (q_head < q_tail && !aborted) {
     const int u = uq[q_head % QN];
     ++q_head;
-    const Unit x = unit_info(p, u);
+    const Unit x = unit_info(p, u, ns);
 
     // Q fragments (m16n8k16 A layout) straight from global memory; rows past the end are 0.
     uint32_t qf[D / 16][4];
@@ -440,7 +443,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
       if constexpr (FP8) {
         // n tiles 2c / 2c + 1 hold the even / odd dims of chunk c: dims 16c + 4t + (0..3)
         // are o[2c][2h], o[2c + 1][2h], o[2c][2h + 1], o[2c + 1][2h + 1].
-        if (p.num_splits == 1) {
+        if (ns == 1) {
           __nv_bfloat16* dst = p.out + (long long)tok * p.o_stride_t + (long long)head * D;
 #pragma unroll
           for (int c = 0; c < D / 16; ++c)
@@ -462,7 +465,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
         }
         continue;
       }
-      if (p.num_splits == 1) {
+      if (ns == 1) {
         __nv_bfloat16* dst = p.out + (long long)tok * p.o_stride_t + (long long)head * D;
 #pragma unroll
         for (int n = 0; n < D / 8; ++n)

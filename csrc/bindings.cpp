@@ -268,7 +268,8 @@ void paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::T
                      const at::Tensor& q_start, const at::Tensor& work, at::Tensor& out,
                      c10::optional<at::Tensor> part_o, c10::optional<at::Tensor> part_lse,
                      c10::optional<at::Tensor> sinks, int64_t num_splits, int64_t num_kv_heads,
-                     int64_t window, double scale, bool decode, double k_scale, double v_scale) {
+                     int64_t window, double scale, bool decode, double k_scale, double v_scale,
+                     c10::optional<at::Tensor> splits_dev) {
   CHECK_CUDA(q);
   CHECK_BF16(q);
   const bool fp8 = k_cache.scalar_type() == at::kFloat8_e4m3fn;
@@ -314,6 +315,10 @@ void paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::T
   p.scale_log2 = (float)(scale * 1.4426950408889634 * (fp8 ? k_scale : 1.0));
   p.kv_fp8 = fp8 ? 1 : 0;
   p.v_scale = fp8 ? (float)v_scale : 1.f;
+  if (splits_dev.has_value()) {
+    TORCH_CHECK(splits_dev->scalar_type() == at::kInt && splits_dev->is_cuda(), "splits_dev must be int32 CUDA");
+    p.splits_dev = splits_dev->data_ptr<int>();
+  }
   p.total_tokens = (int)q.size(0);
   p.status = status_word();
   if (decode && k_cache.is_contiguous() && v_cache.is_contiguous()) {

@@ -116,6 +116,12 @@ def test_paged_decode_tma(cuda_device, D, bs, q_len, window, sinks):
             out = ops.paged_attention(q, kc, vc, bt, sl, qs, work, True, splits, scale,
                                       window=window, sinks=sink_t)
             assert _rel_err(out, ref) < 2e-2, splits
+    # a device-side split factor below the launch's (CUDA-graph decode): 1 and 3 of 24
+    for dev_splits in (1, 3):
+        sd = torch.tensor([dev_splits], dtype=torch.int32, device=cuda_device)
+        out = ops.paged_attention(q, kc, vc, bt, sl, qs, work, True, 24, scale, window=window,
+                                  sinks=sink_t, splits_dev=sd)
+        assert _rel_err(out, ref) < 2e-2, dev_splits
 
 
 @pytest.mark.parametrize("D", [64, 128, 256])

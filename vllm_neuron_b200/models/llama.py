@@ -60,6 +60,7 @@ class ForwardBatch:
     deep_rows: torch.Tensor | None = None    # [n] int64 rows receiving DeepStack features
     deep_feats: torch.Tensor | None = None   # [n_deep, n, H] added after decoder layers 0..n_deep-1
     max_q_len: int = 0                       # longest query of the step (host value; 0 = unknown)
+    splits_dev: torch.Tensor | None = None   # [1] int32 split-KV factor of this decode step
 
 
 def _shard(n: int, world: int, rank: int) -> tuple[int, int]:
@@ -492,7 +493,7 @@ class LlamaForCausalLM(torch.nn.Module):
         ops.paged_attention(q.view(T, self.Hq, self.D), k_cache, v_cache, b.block_tables, b.seq_lens,
                             b.q_start, b.work, b.decode, ns, self.scale, window=window, sinks=sinks,
                             out=attn.view(T, self.Hq, self.D), part_o=part_o, part_lse=part_l,
-                            k_scale=kv_scale[0], v_scale=kv_scale[1])
+                            k_scale=kv_scale[0], v_scale=kv_scale[1], splits_dev=b.splits_dev)
 
     def compute_logits(self, x: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:
         S = idx.shape[0]

@@ -82,12 +82,15 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
                     window: int = 0, sinks: torch.Tensor | None = None,
                     out: torch.Tensor | None = None, part_o: torch.Tensor | None = None,
                     part_lse: torch.Tensor | None = None, k_scale: float = 1.0,
-                    v_scale: float = 1.0) -> torch.Tensor:
+                    v_scale: float = 1.0, splits_dev: torch.Tensor | None = None) -> torch.Tensor:
     """Attention of ``q [T, Hq, D]`` over the paged cache; returns ``out [T, Hq, D]``.
 
     A ``torch.float8_e4m3fn`` cache holds ``K / k_scale`` and ``V / v_scale`` (per-tensor
     scales, the reference's FP8 KV cache: vllm_neuron/utils/dtype_utils.py,
-    functional/attention/attention_decode.py:527-651); the kernels dequantize on load."""
+    functional/attention/attention_decode.py:527-651); the kernels dequantize on load.
+    ``splits_dev`` (int32 on the device, decode only): the split factor to use, at most
+    ``num_splits`` (a CUDA graph captured for the largest context splits each step by its real
+    context lengths)."""
     if out is None:
         out = torch.empty_like(q)
     if not q.is_cuda:
@@ -100,7 +103,7 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
         part_lse = torch.empty((num_splits, T, Hq), dtype=torch.float32, device=q.device)
     ext().paged_attention(q, k_cache, v_cache, block_tables, seq_lens, q_start, work, out,
                           part_o, part_lse, sinks, num_splits, k_cache.shape[1], window, scale,
-                          decode, float(k_scale), float(v_scale))
+                          decode, float(k_scale), float(v_scale), splits_dev)
     return out
 
 

@@ -49,7 +49,7 @@ class Layout:
                         ("seqlen", self.B), ("lidx", self.S), ("work", 2 * self.W),
                         ("bt", self.B * self.nblk), ("temp", self.S), ("topk", self.S),
                         ("topp", self.S), ("minp", self.S), ("seed", 2 * self.S), ("offs", self.S),
-                        ("rslot", self.S), ("sslot", self.B)):
+                        ("rslot", self.S), ("sslot", self.B), ("nsplit", 1)):
             self.off[name] = (o, n)
             o += _round(n)
         self.total = o
@@ -254,9 +254,14 @@ class ModelRunner:
         if pad_B is not None:
             w = ops.build_work(np.ones(Bp, dtype=np.int64), np.full(Bp, self.max_model_len), G, m.Hkv, self.num_sms,
                                max_splits=m.attn_splits_max, head_dim=m.D)
+            # the graph was captured for max_model_len: split this step by its real contexts
+            real = ops.build_work(np.ones(Bp, dtype=np.int64), np.maximum(sl[:Bp], 1).astype(np.int64), G, m.Hkv,
+                                  self.num_sms, max_splits=m.attn_splits_max, head_dim=m.D)
+            h[o["nsplit"][0]] = min(real.num_splits, w.num_splits)
         else:
             w = ops.build_work(q_lens[:Bp], sl[:Bp].astype(np.int64), G, m.Hkv, self.num_sms,
                                max_splits=m.attn_splits_max, head_dim=m.D)
+            h[o["nsplit"][0]] = w.num_splits
         work = h[o["work"][0]:o["work"][0] + 2 * len(w.work)]
         work[:] = w.work.reshape(-1)
         self._last_work_len = len(w.work)
@@ -353,6 +358,7 @@ class ModelRunner:
             logits_indices=sec("lidx", S),
             decode=decode, num_splits=splits, num_tokens=lay.T)
         fb.max_q_len = 1 if decode else getattr(self, "_last_max_q", 0)
+        fb.splits_dev = sec("nsplit", 1) if decode and buf.is_cuda else None
         fb.seq_slots = sec("sslot", B)
         samp = dict(temperature=sec("temp", S, torch.float32), top_k=sec("topk", S),
                     top_p=sec("topp", S, torch.float32), min_p=sec("minp", S, torch.float32),
@@ -443,6 +449,7 @@ class ModelRunner:
             h[o["topp"][0]:o["topp"][0] + b] = torch.tensor([1.0] * b).view(torch.int32)
             h[o["rslot"][0]:o["rslot"][0] + b] = self.pad_slot
             h[o["sslot"][0]:o["sslot"][0] + b] = self.pad_slot
+            h[o["nsplit"][0]] = w.num_splits
             buf.copy_(h)
             fb, samp = self._views(buf, lay, b, b, b, True, w.num_splits)
             tok = torch.zeros(b, dtype=torch.int32, device=self.device)
@@ -504,6 +511,7 @@ class ModelRunner:
         h[o["topp"][0]] = torch.tensor([1.0]).view(torch.int32)
         h[o["rslot"][0]] = self.pad_slot
         h[o["sslot"][0]] = self.pad_slot
+        h[o["nsplit"][0]] = w.num_splits
         buf = self.dev_buf[:lay.total]
         buf.copy_(h)
         fb, _ = self._views(buf, lay, 1, 1, len(w.work), True, w.num_splits)
