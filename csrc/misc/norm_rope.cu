@@ -95,7 +95,7 @@ __device__ __forceinline__ void zero8<__nv_bfloat16>(__nv_bfloat16* p) {
 }
 
 template <typename TX, bool HAS_RES, int NV>
-__global__ void __launch_bounds__(256) add_rmsnorm_kernel(TX* x, long long x_stride,
+__global__ void __launch_bounds__(1024) add_rmsnorm_kernel(TX* x, long long x_stride,
                                                           __nv_bfloat16* residual,
                                                           long long r_stride,
                                                           const __nv_bfloat16* __restrict__ w,
@@ -149,7 +149,9 @@ static void launch_norm(TX* x, long long xs, __nv_bfloat16* res, long long rs,
                         const __nv_bfloat16* w, __nv_bfloat16* out, long long os, int rows, int H,
                         float eps, bool clear, cudaStream_t stream) {
   const int vecs = H / 8;
-  int threads = vecs <= 128 ? ((vecs + 31) / 32) * 32 : (vecs <= 512 ? 128 : 256);
+  // one 8-element vector per thread up to 1024 threads: a row's loads spread over many warps
+  // (decode batches have few rows, so per-row latency dominates)
+  int threads = vecs <= 1024 ? ((vecs + 31) / 32) * 32 : 1024;
   const int nv = (vecs + threads - 1) / threads;
 #define B200_NORM(NV_)                                                                   \
   if (nv <= NV_) {                                                                       \
