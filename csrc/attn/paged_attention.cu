@@ -482,15 +482,28 @@ __global__ void __launch_bounds__(256) attn_combine_warp_kernel(
   float acc[PER];
 #pragma unroll
   for (int e = 0; e < PER; ++e) acc[e] = 0.f;
-  for (int sp = 0; sp < num_splits; ++sp) {
-    const float wgt = __shfl_sync(0xffffffffu, wl, sp);
-    if (wgt == 0.f) continue;  // empty split (uniform over the warp)
-    const float* src = part_o + (sp * split_stride + row) * D + lane * PER;
+  // four splits per iteration: their loads are in flight together (empty splits, weight 0,
+  // are not read: their partials were never written)
+  for (int s0 = 0; s0 < num_splits; s0 += 4) {
+    float wg[4];
+    float2 v[4][PER / 2];
 #pragma unroll
-    for (int e = 0; e < PER; e += 2) {
-      const float2 v = *reinterpret_cast<const float2*>(src + e);
-      acc[e] += wgt * v.x;
-      acc[e + 1] += wgt * v.y;
+    for (int q = 0; q < 4; ++q) {
+      const int sp = s0 + q;
+      wg[q] = __shfl_sync(0xffffffffu, wl, sp < num_splits ? sp : 0);
+      if (sp >= num_splits) wg[q] = 0.f;
+      const float* src = part_o + ((long long)(sp < num_splits ? sp : 0) * split_stride + row) * D + lane * PER;
+#pragma unroll
+      for (int e = 0; e < PER / 2; ++e)
+        v[q][e] = wg[q] != 0.f ? *reinterpret_cast<const float2*>(src + 2 * e) : make_float2(0.f, 0.f);
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+#pragma unroll
+      for (int e = 0; e < PER / 2; ++e) {
+        acc[2 * e] += wg[q] * v[q][e].x;
+        acc[2 * e + 1] += wg[q] * v[q][e].y;
+      }
     }
   }
   __nv_bfloat16* dst = out + (long long)tok * o_stride_t + (long long)head * D + lane * PER;
