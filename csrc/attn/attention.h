@@ -40,7 +40,31 @@ struct PagedAttnParams {
   // device (1 <= *splits_dev <= num_splits).  Lets a captured CUDA graph (whose num_splits is
   // sized for max_model_len) split each step by its real context lengths.
   const int* splits_dev;
+  // Decode context parallelism: this rank holds the tokens of every (dcp_size * block_size)
+  // token window whose block_size-slice index is dcp_rank; seq_lens are then the local token
+  // counts and dcp_seq_lens the whole-sequence lengths (null without DCP), from which each
+  // query's causal limit in local key indices is derived.
+  const int* dcp_seq_lens;
+  int dcp_size, dcp_rank;
+  // Write unnormalised split partials (part_o / part_lse) even for one split and leave the
+  // merge to the caller (DCP merges the partials of all ranks after exchanging them).
+  int partial_out;
 };
+
+#ifdef __CUDACC__
+// Number of tokens among global positions [0, n) that a DCP rank holds (block_size interleave).
+__device__ __forceinline__ int dcp_local_count(int n, int bs, int size, int rank) {
+  const int vb = bs * size;
+  const int full = n / vb;
+  const int rem = n - full * vb;
+  return full * bs + min(max(rem - rank * bs, 0), bs);
+}
+
+// Last local key index visible to the query at global position g (-1: none on this rank).
+__device__ __forceinline__ int dcp_last_visible(int g, int bs, int size, int rank) {
+  return dcp_local_count(g + 1, bs, size, rank) - 1;
+}
+#endif
 
 void paged_attention_launch(const PagedAttnParams& p, int num_work, int head_dim, bool decode,
                             cudaStream_t stream);
@@ -52,5 +76,10 @@ bool paged_decode_tma_supported(const PagedAttnParams& p, int head_dim);
 void paged_decode_tma_launch(const PagedAttnParams& p, int num_work, int head_dim,
                              cudaStream_t stream);
 int paged_decode_warps_per_cta(int head_dim);
+
+// Merge split partials part_o [S, T, Hq, D] / part_lse [S, T, Hq] (log2 domain) into bf16 out.
+void attn_combine_launch(const float* part_o, const float* part_lse, __nv_bfloat16* out,
+                         long long o_stride_t, int total_tokens, int Hq, int num_splits,
+                         int head_dim, cudaStream_t stream);
 
 }  // namespace b200

@@ -121,10 +121,18 @@ __global__ void __launch_bounds__(128)
   const int ctx0 = kv_len - q_len;
   const int rows_total = q_len * G;
   const int rows_here = min(BM, rows_total - row0);
+  // Last visible key (local index) of query i of this sequence: causal in global positions,
+  // mapped onto this rank's tokens under decode context parallelism.
+  const int ctx0g = p.dcp_seq_lens != nullptr ? p.dcp_seq_lens[b] - q_len : 0;
+  auto last_key = [&](int i) -> int {
+    return p.dcp_seq_lens != nullptr
+               ? dcp_last_visible(ctx0g + i, p.block_size, p.dcp_size, p.dcp_rank)
+               : ctx0 + i;
+  };
 
   // Visible KV range of the whole tile.
-  const int p_min = ctx0 + row0 / G;
-  const int p_max = ctx0 + (row0 + rows_here - 1) / G;
+  const int p_min = last_key(row0 / G);
+  const int p_max = last_key((row0 + rows_here - 1) / G);
   int lo = 0;
   if (p.window > 0) lo = max(0, p_min - p.window + 1);
   const int hi = min(p_max + 1, kv_len);
@@ -213,7 +221,7 @@ __global__ void __launch_bounds__(128)
     const int r = wrow + (lane >> 2) + h * 8;
     rvalid[h] = r < rows_here;
     const int pr = row0 + r;
-    qpos[h] = ctx0 + pr / G;
+    qpos[h] = last_key(pr / G);
     m_r[h] = -INFINITY;
     l_r[h] = 0.f;
     // The sink joins the softmax once, in split 0 (and in decode mode in warp 0 only).
@@ -374,7 +382,7 @@ __global__ void __launch_bounds__(128)
         for (int ww = 0; ww < 4; ++ww) v += sm_o[(ww * 16 + r) * D + c0 + c] * f[ww];
         acc[c] = v * inv;
       }
-      if (p.num_splits == 1) {
+      if (p.num_splits == 1 && !p.partial_out) {
         __nv_bfloat16* dst = p.out + (long long)tok * p.o_stride_t + (long long)head * D + c0;
         uint4 v0 = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
                               pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
@@ -399,7 +407,7 @@ __global__ void __launch_bounds__(128)
       const int tok = q_begin + pr / G;
       const int head = kvh * G + pr % G;
       const float inv = (l_r[h] > 0.f ? 1.f / l_r[h] : 0.f) * (FP8 ? p.v_scale : 1.f);
-      if (p.num_splits == 1) {
+      if (p.num_splits == 1 && !p.partial_out) {
         __nv_bfloat16* dst = p.out + (long long)tok * p.o_stride_t + (long long)head * D;
 #pragma unroll
         for (int n = 0; n < D / 8; ++n) {
@@ -533,13 +541,41 @@ static void launch_attn(const PagedAttnParams& p, int num_work, cudaStream_t str
     launch_attn_t<D, DECODE, false>(p, num_work, stream);
 }
 
+static void combine_splits(const float* po, const float* pl, __nv_bfloat16* out,
+                           long long o_stride_t, int total_tokens, int Hq, int num_splits,
+                           int head_dim, const int* splits_dev, cudaStream_t stream) {
+  if (num_splits <= 32) {
+    const dim3 grid((unsigned)((total_tokens * Hq + 7) / 8));
+    if (head_dim == 128)
+      launch_pdl(attn_combine_warp_kernel<128>, grid, dim3(256), 0, stream, po, pl, out,
+                 o_stride_t, total_tokens, Hq, num_splits, splits_dev);
+    else if (head_dim == 256)
+      launch_pdl(attn_combine_warp_kernel<256>, grid, dim3(256), 0, stream, po, pl, out,
+                 o_stride_t, total_tokens, Hq, num_splits, splits_dev);
+    else
+      launch_pdl(attn_combine_warp_kernel<64>, grid, dim3(256), 0, stream, po, pl, out,
+                 o_stride_t, total_tokens, Hq, num_splits, splits_dev);
+  } else {
+    dim3 grid(total_tokens, Hq);
+    if (head_dim == 128)
+      launch_pdl(attn_combine_kernel<128>, grid, dim3(128), 0, stream, po, pl, out, o_stride_t,
+                 total_tokens, Hq, num_splits);
+    else if (head_dim == 256)
+      launch_pdl(attn_combine_kernel<256>, grid, dim3(256), 0, stream, po, pl, out, o_stride_t,
+                 total_tokens, Hq, num_splits);
+    else
+      launch_pdl(attn_combine_kernel<64>, grid, dim3(64), 0, stream, po, pl, out, o_stride_t,
+                 total_tokens, Hq, num_splits);
+  }
+}
+
 void paged_attention_launch(const PagedAttnParams& p_in, int num_work, int head_dim, bool decode,
                             cudaStream_t stream) {
   if (num_work == 0) return;
   PagedAttnParams p = p_in;
   const bool tma = decode && paged_decode_tma_supported(p, head_dim);
   // device split factors are a feature of the TMA decode path with the warp combine (<= 32)
-  if (!tma || p.num_splits > 32) p.splits_dev = nullptr;
+  if (!tma || p.num_splits > 32 || p.partial_out) p.splits_dev = nullptr;
   if (tma) {
     paged_decode_tma_launch(p, num_work, head_dim, stream);
   } else if (head_dim == 128) {
@@ -554,31 +590,19 @@ void paged_attention_launch(const PagedAttnParams& p_in, int num_work, int head_
     throw std::invalid_argument("paged_attention: unsupported head_dim " +
                                 std::to_string(head_dim));
   }
-  if (p.num_splits > 1 && p.num_splits <= 32) {
-    const dim3 grid((unsigned)((p.total_tokens * p.Hq + 7) / 8));
-    const float* po = p.part_o;
-    const float* pl = p.part_lse;
-    if (head_dim == 128)
-      launch_pdl(attn_combine_warp_kernel<128>, grid, dim3(256), 0, stream, po, pl, p.out,
-                 p.o_stride_t, p.total_tokens, p.Hq, p.num_splits, p.splits_dev);
-    else if (head_dim == 256)
-      launch_pdl(attn_combine_warp_kernel<256>, grid, dim3(256), 0, stream, po, pl, p.out,
-                 p.o_stride_t, p.total_tokens, p.Hq, p.num_splits, p.splits_dev);
-    else
-      launch_pdl(attn_combine_warp_kernel<64>, grid, dim3(256), 0, stream, po, pl, p.out,
-                 p.o_stride_t, p.total_tokens, p.Hq, p.num_splits, p.splits_dev);
-  } else if (p.num_splits > 1) {
-    dim3 grid(p.total_tokens, p.Hq);
-    if (head_dim == 128)
-      launch_pdl(attn_combine_kernel<128>, grid, dim3(128), 0, stream, (const float*)p.part_o,
-                 (const float*)p.part_lse, p.out, p.o_stride_t, p.total_tokens, p.Hq, p.num_splits);
-    else if (head_dim == 256)
-      launch_pdl(attn_combine_kernel<256>, grid, dim3(256), 0, stream, (const float*)p.part_o,
-                 (const float*)p.part_lse, p.out, p.o_stride_t, p.total_tokens, p.Hq, p.num_splits);
-    else
-      launch_pdl(attn_combine_kernel<64>, grid, dim3(64), 0, stream, (const float*)p.part_o,
-                 (const float*)p.part_lse, p.out, p.o_stride_t, p.total_tokens, p.Hq, p.num_splits);
-  }
+  if (p.num_splits > 1 && !p.partial_out)
+    combine_splits(p.part_o, p.part_lse, p.out, p.o_stride_t, p.total_tokens, p.Hq,
+                   p.num_splits, head_dim, p.splits_dev, stream);
+}
+
+void attn_combine_launch(const float* part_o, const float* part_lse, __nv_bfloat16* out,
+                         long long o_stride_t, int total_tokens, int Hq, int num_splits,
+                         int head_dim, cudaStream_t stream) {
+  if (total_tokens == 0) return;
+  if (head_dim != 64 && head_dim != 128 && head_dim != 256)
+    throw std::invalid_argument("attn_combine: unsupported head_dim " + std::to_string(head_dim));
+  combine_splits(part_o, part_lse, out, o_stride_t, total_tokens, Hq, num_splits, head_dim,
+                 nullptr, stream);
 }
 
 }  // namespace b200

@@ -102,6 +102,14 @@ struct Unit {
   int s_lo, s_hi;  // tile range [s_lo, s_hi) of 16-token tiles
 };
 
+// Last visible key (local index) of packed query i of unit x; under decode context
+// parallelism the causal limit is taken in global positions and mapped to this rank's tokens.
+__device__ __forceinline__ int unit_last_key(const PagedAttnParams& p, const Unit& x, int i) {
+  if (p.dcp_seq_lens == nullptr) return x.ctx0 + i;
+  const int q_len = p.q_start[x.b + 1] - x.q_begin;
+  return dcp_last_visible(p.dcp_seq_lens[x.b] - q_len + i, p.block_size, p.dcp_size, p.dcp_rank);
+}
+
 __device__ __forceinline__ Unit unit_info(const PagedAttnParams& p, int u, int ns) {
   Unit x;
   const int per_item = p.Hkv * ns;
@@ -117,8 +125,8 @@ __device__ __forceinline__ Unit unit_info(const PagedAttnParams& p, int u, int n
   x.kv_len = p.seq_lens[x.b];
   x.ctx0 = x.kv_len - q_len;
   x.rows_here = min(16, q_len * p.G - x.row0);
-  x.p_min = x.ctx0 + x.row0 / p.G;
-  x.p_max = x.ctx0 + (x.row0 + x.rows_here - 1) / p.G;
+  x.p_min = unit_last_key(p, x, x.row0 / p.G);
+  x.p_max = unit_last_key(p, x, (x.row0 + x.rows_here - 1) / p.G);
   int lo = 0;
   if (p.window > 0) lo = max(0, x.p_min - p.window + 1);
   const int hi = min(x.p_max + 1, x.kv_len);
@@ -172,6 +180,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
   int* sched = p.sched;
   // split factor of this step (device value under CUDA graphs, else the launch's)
   const int ns = p.splits_dev != nullptr ? max(1, min(*p.splits_dev, p.num_splits)) : p.num_splits;
+  const bool direct = ns == 1 && !p.partial_out;  // bf16 output without a split merge
   const int num_units = num_units_max / p.num_splits * ns;
   uint64_t policy = 0;
   if (lane == 0) policy = policy_evict_first();  // each K/V byte is read once per step
@@ -215,7 +224,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
       const Unit x = unit_info(p, u, ns);
       if (x.s_lo >= x.s_hi) {
         // empty split: its partial carries no weight in the combine
-        if (ns > 1 && lane < x.rows_here) {
+        if (!direct && lane < x.rows_here) {
           const int pr = x.row0 + lane;
           const int tok = x.q_begin + pr / p.G;
           const int head = x.kvh * p.G + pr % p.G;
@@ -260,7 +269,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
       const int pr = x.row0 + (rvalid[h] ? r : 0);
       qrow_tok[h] = x.q_begin + pr / p.G;
       qrow_head[h] = x.kvh * p.G + pr % p.G;
-      qpos[h] = x.ctx0 + pr / p.G;
+      qpos[h] = unit_last_key(p, x, pr / p.G);
       m_r[h] = -INFINITY;
       l_r[h] = 0.f;
       if (p.sinks != nullptr && x.split == 0 && rvalid[h]) {
@@ -443,7 +452,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
       if constexpr (FP8) {
         // n tiles 2c / 2c + 1 hold the even / odd dims of chunk c: dims 16c + 4t + (0..3)
         // are o[2c][2h], o[2c + 1][2h], o[2c][2h + 1], o[2c + 1][2h + 1].
-        if (ns == 1) {
+        if (direct) {
           __nv_bfloat16* dst = p.out + (long long)tok * p.o_stride_t + (long long)head * D;
 #pragma unroll
           for (int c = 0; c < D / 16; ++c)
@@ -465,7 +474,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
         }
         continue;
       }
-      if (ns == 1) {
+      if (direct) {
         __nv_bfloat16* dst = p.out + (long long)tok * p.o_stride_t + (long long)head * D;
 #pragma unroll
         for (int n = 0; n < D / 8; ++n)

@@ -269,7 +269,8 @@ void paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::T
                      c10::optional<at::Tensor> part_o, c10::optional<at::Tensor> part_lse,
                      c10::optional<at::Tensor> sinks, int64_t num_splits, int64_t num_kv_heads,
                      int64_t window, double scale, bool decode, double k_scale, double v_scale,
-                     c10::optional<at::Tensor> splits_dev) {
+                     c10::optional<at::Tensor> splits_dev, c10::optional<at::Tensor> dcp_seq_lens,
+                     int64_t dcp_size, int64_t dcp_rank, bool partial_out) {
   CHECK_CUDA(q);
   CHECK_BF16(q);
   const bool fp8 = k_cache.scalar_type() == at::kFloat8_e4m3fn;
@@ -300,8 +301,12 @@ void paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::T
   p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   p.o_stride_t = out.stride(0);
   p.num_splits = (int)num_splits;
-  if (num_splits > 1) {
+  p.partial_out = partial_out ? 1 : 0;
+  if (num_splits > 1 || partial_out) {
     TORCH_CHECK(part_o.has_value() && part_lse.has_value(), "split-KV needs partial buffers");
+    TORCH_CHECK(part_o->scalar_type() == at::kFloat && part_lse->scalar_type() == at::kFloat,
+                "partials must be float32");
+    TORCH_CHECK(part_lse->numel() >= num_splits * q.size(0) * q.size(1), "part_lse too small");
     TORCH_CHECK(part_o->numel() >= num_splits * q.size(0) * q.size(1) * D, "part_o too small");
     p.part_o = part_o->data_ptr<float>();
     p.part_lse = part_lse->data_ptr<float>();
@@ -319,6 +324,16 @@ void paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::T
     TORCH_CHECK(splits_dev->scalar_type() == at::kInt && splits_dev->is_cuda(), "splits_dev must be int32 CUDA");
     p.splits_dev = splits_dev->data_ptr<int>();
   }
+  if (dcp_seq_lens.has_value()) {
+    TORCH_CHECK(dcp_seq_lens->scalar_type() == at::kInt && dcp_seq_lens->is_cuda(),
+                "dcp_seq_lens must be int32 CUDA");
+    TORCH_CHECK(dcp_size >= 1 && dcp_rank >= 0 && dcp_rank < dcp_size, "bad DCP rank / size");
+    TORCH_CHECK(window == 0 && !sinks.has_value(),
+                "decode context parallelism supports neither sliding windows nor sinks");
+    p.dcp_seq_lens = dcp_seq_lens->data_ptr<int>();
+    p.dcp_size = (int)dcp_size;
+    p.dcp_rank = (int)dcp_rank;
+  }
   p.total_tokens = (int)q.size(0);
   p.status = status_word();
   if (decode && k_cache.is_contiguous() && v_cache.is_contiguous()) {
@@ -327,7 +342,28 @@ void paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::T
   }
   const int num_work = (int)work.size(0);
   b200::paged_attention_launch(p, num_work, D, decode, cur_stream());
-  check_launch("paged_attention", num_work == 0 ? 0 : (num_splits > 1 ? 2 : 1));
+  check_launch("paged_attention", num_work == 0 ? 0 : (num_splits > 1 && !partial_out ? 2 : 1));
+}
+
+// Merge split partials part_o [S, T, Hq, D] / part_lse [S, T, Hq] into out [T, Hq, D] bf16.
+void attn_combine(const at::Tensor& part_o, const at::Tensor& part_lse, at::Tensor& out) {
+  CHECK_CUDA(part_o);
+  CHECK_BF16(out);
+  TORCH_CHECK(part_o.scalar_type() == at::kFloat && part_lse.scalar_type() == at::kFloat,
+              "partials must be float32");
+  TORCH_CHECK(part_o.dim() == 4 && part_o.is_contiguous() && part_lse.is_contiguous(),
+              "part_o must be a contiguous [S, T, Hq, D] tensor");
+  TORCH_CHECK(out.dim() == 3 && out.stride(2) == 1 && out.stride(1) == out.size(2),
+              "out heads must be packed");
+  const int S = (int)part_o.size(0), T = (int)part_o.size(1), Hq = (int)part_o.size(2),
+            D = (int)part_o.size(3);
+  TORCH_CHECK(out.size(0) == T && out.size(1) == Hq && out.size(2) == D, "out shape mismatch");
+  TORCH_CHECK(part_lse.numel() == (int64_t)S * T * Hq, "part_lse shape mismatch");
+  const c10::cuda::CUDAGuard guard(part_o.device());
+  b200::attn_combine_launch(part_o.data_ptr<float>(), part_lse.data_ptr<float>(),
+                            reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0), T, Hq,
+                            S, D, cur_stream());
+  check_launch("attn_combine");
 }
 
 void add_rmsnorm(at::Tensor& x, c10::optional<at::Tensor> residual, const at::Tensor& w,
@@ -870,6 +906,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sp_norm_push", &sp_norm_push);
   m.def("sp_wait", &sp_wait);
   m.def("paged_attention", &paged_attention);
+  m.def("attn_combine", &attn_combine);
   m.def("add_rmsnorm", &add_rmsnorm);
   m.def("rope_kv_write", &rope_kv_write);
   m.def("silu_mul", &silu_mul);

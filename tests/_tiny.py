@@ -19,11 +19,11 @@ def tiny_llama_config(**over):
 
 
 @functools.lru_cache(maxsize=4)
-def tiny_llama_checkpoint(seed: int = 0):
+def tiny_llama_checkpoint(seed: int = 0, num_key_value_heads: int = 2):
     from transformers import LlamaForCausalLM
 
     torch.manual_seed(seed)
-    hf = LlamaForCausalLM(tiny_llama_config()).float().eval()
+    hf = LlamaForCausalLM(tiny_llama_config(num_key_value_heads=num_key_value_heads)).float().eval()
     d = tempfile.mkdtemp(prefix="tiny_llama_")
     hf.save_pretrained(d, safe_serialization=True)
     return d, hf

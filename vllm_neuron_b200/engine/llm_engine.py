@@ -49,6 +49,9 @@ class EngineArgs:
     # {"method": "ngram" | "eagle3", "num_speculative_tokens": k, "model": draft checkpoint,
     #  "prompt_lookup_min"/"prompt_lookup_max": n-gram sizes}
     speculative_config: dict | None = None
+    # decode context parallelism: every sequence's KV is token-sharded over this many
+    # consecutive TP ranks (which share replicated KV heads)
+    decode_context_parallel_size: int = 1
 
 
 @dataclass
@@ -174,13 +177,31 @@ def _kv_scales_from_checkpoint(model, model_path) -> list[tuple[float, float]] |
     return out
 
 
+def validate_dcp(arch, model, tp: GroupComm, dcp: int):
+    """Decode context parallelism needs replicated KV heads shared by each replica set of
+    ``dcp`` consecutive TP ranks, and a model whose attention is full causal softmax attention
+    (no sliding window, sinks or linear-attention state) (reference: DCP constraints,
+    vllm_neuron/vllm/platform.py:600-660)."""
+    W, hkv = tp.world, arch.num_kv_heads
+    if W % dcp:
+        raise ValueError(f"decode_context_parallel_size={dcp} must divide TP={W}")
+    if not (W > hkv and (W // hkv) % dcp == 0):
+        raise ValueError(f"DCP={dcp} needs TP={W} > num_kv_heads={hkv} with DCP dividing "
+                         f"TP / num_kv_heads (the ranks of a replica set share their KV heads)")
+    if not getattr(model, "supports_dcp", False):
+        raise NotImplementedError(f"{type(model).__name__} does not support decode context "
+                                  "parallelism (sliding windows, sinks or linear attention)")
+
+
 def build_runner(args: EngineArgs, model, max_model_len: int, device, b200_config):
-    """The model runner of ``model`` (KV cache not yet allocated)."""
+    """The model runner of ``model`` (KV cache not yet allocated).  Its (scheduler) block size
+    is the cache block size times the DCP size."""
     from ..worker.model_runner import ModelRunner
 
     return ModelRunner(model, max_num_seqs=args.max_num_seqs,
                        max_num_batched_tokens=max(args.max_num_batched_tokens, args.max_num_seqs),
-                       max_model_len=max_model_len, block_size=args.block_size,
+                       max_model_len=max_model_len,
+                       block_size=args.block_size * max(1, args.decode_context_parallel_size),
                        cuda_graphs=(args.cuda_graphs and b200_config.cuda_graphs
                                     and getattr(model, "supports_cuda_graphs", True)),
                        device=device, seed=args.seed)
@@ -196,6 +217,17 @@ class LLMEngine:
         real_group = tp.world > 1 and tp.group is not None
         self.runner = build_runner(args, self.model, self.max_model_len, self.device, self.b200_config)
         self.runner.sampling_dp = bool(self.b200_config.sampling_dp)
+        dcp = max(1, int(args.decode_context_parallel_size or 1))
+        if dcp > 1:
+            from ..parallel import state as _ps
+
+            validate_dcp(self.arch, self.model, tp, dcp)
+            group = _ps.get_parallel_state().dcp
+            if group.world != dcp:
+                raise ValueError("the parallel state has no DCP group of this size "
+                                 "(pass decode_context_parallel_size to the LLM front end)")
+            self.model.dcp = group
+            self.runner.set_dcp(dcp, group.rank)
         nb = args.num_gpu_blocks or self.runner.profile_num_blocks(args.gpu_memory_utilization)
         if real_group and self.device.type == "cuda":
             t = torch.tensor([nb], dtype=torch.int64, device=self.device)
@@ -206,7 +238,7 @@ class LLMEngine:
         # Models with per-request recurrent state (linear attention) cannot reuse cached KV
         # prefixes: the state after the prefix is not stored with the blocks.
         apc = args.enable_prefix_caching and getattr(self.model, "supports_prefix_caching", True)
-        self.block_manager = BlockManager(nb, args.block_size, apc)
+        self.block_manager = BlockManager(nb, self.runner.block_size, apc)
         self.scheduler = Scheduler(self.block_manager, args.max_num_seqs, max_tok, self.max_model_len,
                                    enable_chunked_prefill=args.enable_chunked_prefill,
                                    num_batched_tokens_buckets=self.b200_config.num_batched_tokens_buckets,

@@ -54,7 +54,7 @@ class LLM:
                  data_parallel_size: int | None = None, mm_processor_kwargs: dict | None = None,
                  kv_cache_dtype: str = "auto", enable_expert_parallel: bool = False,
                  kv_transfer_config: dict | None = None, ec_transfer_config: dict | None = None,
-                 **unused):
+                 decode_context_parallel_size: int = 1, **unused):
         if device is None:
             device = f"cuda:{torch.cuda.current_device()}" if torch.cuda.is_available() else "cpu"
         ps.init_distributed(backend="gloo" if str(device).startswith("cpu") else None)
@@ -67,7 +67,8 @@ class LLM:
                              f"{world} ranks give {dp}")
         st = ps.initialize_parallel_state(ps.ParallelConfig(world_size=world,
                                                             tensor_parallel_size=tensor_parallel_size,
-                                                            data_parallel_size=dp))
+                                                            data_parallel_size=dp,
+                                                            decode_context_parallel_size=decode_context_parallel_size))
         # Data parallelism: each group of TP ranks is an independent engine replica serving
         # every dp-th request; outputs are gathered over the DP group (reference: data
         # parallel replicas, docs/design/parallelism/data_parallelism.md).
@@ -103,7 +104,8 @@ class LLM:
                           cuda_graphs=not enforce_eager, async_scheduling=async_scheduling,
                           additional_config=additional_config or {},
                           speculative_config=speculative_config, kv_cache_dtype=kv_cache_dtype,
-                          kv_transfer_config=kv_transfer_config)
+                          kv_transfer_config=kv_transfer_config,
+                          decode_context_parallel_size=decode_context_parallel_size)
         self.engine = LLMEngine(args, tp=st.tp)
         self.mm_processor_kwargs = mm_processor_kwargs
         self.tokenizer = None

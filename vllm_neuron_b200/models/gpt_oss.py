@@ -67,6 +67,7 @@ def _quant_experts(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
 
 
 class GptOssForCausalLM(MoEMixin, LlamaForCausalLM):
+    supports_dcp = False  # sinks / sliding windows / linear-attention state
     route_mode = M.ROUTE_TOPK_SOFTMAX
     expert_act = M.ACT_GPTOSS
     renorm = True

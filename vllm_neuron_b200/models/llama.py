@@ -61,6 +61,7 @@ class ForwardBatch:
     deep_feats: torch.Tensor | None = None   # [n_deep, n, H] added after decoder layers 0..n_deep-1
     max_q_len: int = 0                       # longest query of the step (host value; 0 = unknown)
     splits_dev: torch.Tensor | None = None   # [1] int32 split-KV factor of this decode step
+    seq_lens_local: torch.Tensor | None = None  # [B] int32 tokens held by this DCP rank
 
 
 def _shard(n: int, world: int, rank: int) -> tuple[int, int]:
@@ -71,6 +72,7 @@ def _shard(n: int, world: int, rank: int) -> tuple[int, int]:
 
 class LlamaForCausalLM(torch.nn.Module):
     """Dense Llama-3 / Qwen3 decoder (the ``LlamaForCausalLM`` / ``Qwen3ForCausalLM`` archs)."""
+    supports_dcp = True  # decode context parallelism (token-sharded KV)
 
     def __init__(self, cfg: ModelArchConfig, tp: GroupComm = SINGLE, device="cuda",
                  dtype=torch.bfloat16, max_tokens: int = 8192, max_decode_tokens: int = 128,
@@ -121,6 +123,7 @@ class LlamaForCausalLM(torch.nn.Module):
         self.kv_caches: list[tuple[torch.Tensor, torch.Tensor]] = []
         self._alloc_workspace(max_tokens, max_decode_tokens, max_seqs)
         self.tp_fused = None  # TPFusedComm: fused all-reduce + residual + RMSNorm (decode)
+        self.dcp = SINGLE     # decode-context-parallel replica set (KV tokens sharded over it)
         self.sequence_parallel = False  # prefill residual stream sharded over tokens (TP > 1)
         self.mrope_section = None       # (t, h, w) frequency split of the multimodal RoPE
         self._sp = None                 # (padded tokens, local tokens) of the running SP forward
@@ -486,6 +489,8 @@ class LlamaForCausalLM(torch.nn.Module):
                    kv_scale: tuple[float, float] = (1.0, 1.0)):
         T = b.num_tokens
         ns = b.num_splits
+        if self.dcp.world > 1:
+            return self._attention_dcp(q, attn, k_cache, v_cache, b, kv_scale)
         part_o = part_l = None
         if ns > 1:
             part_o = self.ws_part_o[: ns * T * self.Hq * self.D].view(ns, T, self.Hq, self.D)
@@ -494,6 +499,31 @@ class LlamaForCausalLM(torch.nn.Module):
                             b.q_start, b.work, b.decode, ns, self.scale, window=window, sinks=sinks,
                             out=attn.view(T, self.Hq, self.D), part_o=part_o, part_lse=part_l,
                             k_scale=kv_scale[0], v_scale=kv_scale[1], splits_dev=b.splits_dev)
+
+    def _attention_dcp(self, q, attn, k_cache, v_cache, b: ForwardBatch,
+                       kv_scale: tuple[float, float]):
+        """Decode context parallelism: this rank's cache holds one block-size slice of every
+        ``dcp * block_size`` token window.  Q is all-gathered over the replica set (whose ranks
+        share the KV heads), every rank attends over its own tokens and writes unmerged
+        partials, one all-to-all hands each rank the partials of its own heads and the split
+        merge kernel combines them by log-sum-exp (reference: all-gather Q, local attention,
+        all-gather LSE, correction and reduce-scatter over heads,
+        functional/attention/attention_decode.py:902-1062)."""
+        d = self.dcp
+        T, Hq, D, ns, W = b.num_tokens, self.Hq, self.D, b.num_splits, self.dcp.world
+        qg = d.all_gather(q.view(T, Hq, D), dim=1)  # [T, W * Hq, D], heads in rank order
+        dev = q.device
+        po = torch.empty((ns, T, W * Hq, D), dtype=torch.float32, device=dev)
+        pl = torch.empty((ns, T, W * Hq), dtype=torch.float32, device=dev)
+        ops.paged_attention_partial(qg, k_cache, v_cache, b.block_tables, b.seq_lens_local,
+                                    b.q_start, b.work, b.decode, ns, self.scale, po, pl,
+                                    k_scale=kv_scale[0], v_scale=kv_scale[1],
+                                    dcp_seq_lens=b.seq_lens, dcp_size=W, dcp_rank=d.rank)
+        # chunk k of dim 0 (heads of rank k) goes to rank k; chunk k received comes from rank k
+        ro = d.all_to_all(po.view(ns, T, W, Hq, D).permute(2, 0, 1, 3, 4).contiguous())
+        rl = d.all_to_all(pl.view(ns, T, W, Hq).permute(2, 0, 1, 3).contiguous())
+        ops.attn_combine(ro.view(W * ns, T, Hq, D), rl.view(W * ns, T, Hq),
+                         out=attn.view(T, Hq, D))
 
     def compute_logits(self, x: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:
         S = idx.shape[0]

@@ -103,26 +103,92 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
         part_lse = torch.empty((num_splits, T, Hq), dtype=torch.float32, device=q.device)
     ext().paged_attention(q, k_cache, v_cache, block_tables, seq_lens, q_start, work, out,
                           part_o, part_lse, sinks, num_splits, k_cache.shape[1], window, scale,
-                          decode, float(k_scale), float(v_scale), splits_dev)
+                          decode, float(k_scale), float(v_scale), splits_dev, None, 1, 0, False)
+    return out
+
+
+def dcp_local_count(n: int, block_size: int, dcp_size: int, dcp_rank: int) -> int:
+    """Tokens among global positions ``[0, n)`` held by DCP rank ``dcp_rank``: every window of
+    ``dcp_size * block_size`` positions gives each rank one ``block_size`` slice, in rank order
+    (the reference's interleave with ``cp_kv_cache_interleave_size == block_size``:
+    docs/design/parallelism/dcp.md, "local_filled Computation")."""
+    vb = block_size * dcp_size
+    full, rem = divmod(int(n), vb)
+    return full * block_size + min(max(rem - dcp_rank * block_size, 0), block_size)
+
+
+def paged_attention_partial(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                            block_tables: torch.Tensor, seq_lens: torch.Tensor,
+                            q_start: torch.Tensor, work: torch.Tensor, decode: bool,
+                            num_splits: int, scale: float, part_o: torch.Tensor,
+                            part_lse: torch.Tensor, k_scale: float = 1.0, v_scale: float = 1.0,
+                            dcp_seq_lens: torch.Tensor | None = None, dcp_size: int = 1,
+                            dcp_rank: int = 0) -> None:
+    """Unmerged attention partials ``part_o [S, T, Hq, D]`` (each normalised over its split)
+    and ``part_lse [S, T, Hq]`` (log2-sum-exp of the scaled scores, ``-inf`` for an empty
+    split); merge them with :func:`attn_combine`.
+
+    Under decode context parallelism ``seq_lens`` are this rank's local token counts and
+    ``dcp_seq_lens`` the whole-sequence lengths: each query sees the local keys whose global
+    position is at most its own (reference: functional/attention/attention_decode.py:902-1062
+    computes the local output and LSE before the cross-rank correction)."""
+    if not q.is_cuda:
+        o, lse = paged_attention_ref(q, k_cache, v_cache, block_tables, seq_lens, q_start, scale,
+                                     k_scale=k_scale, v_scale=v_scale, dcp_seq_lens=dcp_seq_lens,
+                                     dcp_size=dcp_size, dcp_rank=dcp_rank, return_lse=True)
+        part_o[0].copy_(o)
+        part_lse[0].copy_(lse)
+        part_lse[1:num_splits].fill_(float("-inf"))
+        part_o[1:num_splits].zero_()
+        return
+    ext().paged_attention(q, k_cache, v_cache, block_tables, seq_lens, q_start, work, q,
+                          part_o, part_lse, None, num_splits, k_cache.shape[1], 0, scale,
+                          decode, float(k_scale), float(v_scale), None, dcp_seq_lens,
+                          int(dcp_size), int(dcp_rank), True)
+
+
+def attn_combine(part_o: torch.Tensor, part_lse: torch.Tensor,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    """Merge partials ``[S, T, Hq, D]`` / ``[S, T, Hq]`` (log2 domain) into ``out [T, Hq, D]``:
+    ``out = sum_s 2^(lse_s - M) O_s / sum_s 2^(lse_s - M)``."""
+    S, T, Hq, D = part_o.shape
+    if out is None:
+        out = torch.empty((T, Hq, D), dtype=torch.bfloat16, device=part_o.device)
+    if not part_o.is_cuda:
+        m = part_lse.amax(0, keepdim=True)
+        m = torch.where(torch.isfinite(m), m, torch.zeros_like(m))
+        w = torch.exp2(part_lse - m)
+        den = w.sum(0)
+        o = (w[..., None] * part_o).sum(0) / den.clamp_min(1e-30)[..., None]
+        out.copy_(o.to(out.dtype))
+        return out
+    ext().attn_combine(part_o.contiguous(), part_lse.contiguous(), out)
     return out
 
 
 def paged_attention_ref(q, k_cache, v_cache, block_tables, seq_lens, q_start, scale,
-                        window=0, sinks=None, k_scale=1.0, v_scale=1.0) -> torch.Tensor:
+                        window=0, sinks=None, k_scale=1.0, v_scale=1.0, dcp_seq_lens=None,
+                        dcp_size=1, dcp_rank=0, return_lse=False):
     """fp32 oracle: gathers each sequence's KV from its blocks and runs masked softmax
-    (an fp8 cache is dequantized with its per-tensor scales)."""
+    (an fp8 cache is dequantized with its per-tensor scales).  With ``dcp_seq_lens`` the cache
+    holds one DCP rank's tokens (``seq_lens`` local counts) and the causal mask is taken in
+    global positions; ``return_lse`` also returns the log2-sum-exp of the scaled scores."""
     fp8 = k_cache.dtype == torch.float8_e4m3fn
     ks, vs = (float(k_scale), float(v_scale)) if fp8 else (1.0, 1.0)
     T, Hq, D = q.shape
     Hkv, bs = k_cache.shape[1], k_cache.shape[2]
     G = Hq // Hkv
     out = torch.zeros((T, Hq, D), dtype=torch.float32, device=q.device)
+    lse_out = torch.full((T, Hq), float("-inf"), dtype=torch.float32, device=q.device)
     qs = q_start.tolist()
     sl = seq_lens.tolist()
+    gl = dcp_seq_lens.tolist() if dcp_seq_lens is not None else sl
     bt = block_tables.cpu()
     for b in range(len(sl)):
         q0, q1, L = qs[b], qs[b + 1], sl[b]
         if q1 == q0:
+            continue
+        if L == 0:
             continue
         nblk = (L + bs - 1) // bs
         blocks = bt[b, :nblk].to(k_cache.device).long()
@@ -133,8 +199,12 @@ def paged_attention_ref(q, k_cache, v_cache, block_tables, seq_lens, q_start, sc
         qq = q[q0:q1].float().permute(1, 0, 2)  # [Hq, n, D]
         s = torch.einsum("hnd,hld->hnl", qq, k) * scale
         n = q1 - q0
-        pos = torch.arange(L - n, L, device=q.device)[:, None]
-        j = torch.arange(L, device=q.device)[None, :]
+        Lg = gl[b]
+        pos = torch.arange(Lg - n, Lg, device=q.device)[:, None]
+        j = torch.arange(L, device=q.device)
+        if dcp_seq_lens is not None:  # global position of each local key
+            j = (j // bs) * bs * dcp_size + dcp_rank * bs + j % bs
+        j = j[None, :]
         mask = j <= pos
         if window and window > 0:
             mask = mask & (j > pos - window)
@@ -145,8 +215,11 @@ def paged_attention_ref(q, k_cache, v_cache, block_tables, seq_lens, q_start, sc
             p = torch.softmax(s, dim=-1)[..., :-1]
         else:
             p = torch.softmax(s, dim=-1)
+        p = torch.nan_to_num(p, nan=0.0)  # rows without a visible key (DCP)
         out[q0:q1] = torch.einsum("hnl,hld->hnd", p, v).permute(1, 0, 2)
-    return out
+        if return_lse:
+            lse_out[q0:q1] = (torch.logsumexp(s, dim=-1) * (1.0 / math.log(2.0))).permute(1, 0)
+    return (out, lse_out) if return_lse else out
 
 
 def quantize_kv_fp8(x: torch.Tensor, scale: float) -> torch.Tensor:

@@ -68,6 +68,14 @@ def dcp_groups(tp_group: list[int], dcp: int) -> tuple[list[list[int]], list[lis
     return kv, head
 
 
+def dcp_decode_groups(tp_group: list[int], dcp: int) -> list[list[int]]:
+    """Decode-context-parallel replica sets: ``dcp`` consecutive TP ranks, which share their
+    (replicated) KV heads when TP exceeds the KV head count, split the tokens of every sequence
+    (``dcp_rank = tp_rank % dcp``; reference: docs/design/parallelism/dcp.md, "DCP Decode")."""
+    assert len(tp_group) % dcp == 0
+    return [tp_group[i:i + dcp] for i in range(0, len(tp_group), dcp)]
+
+
 @dataclass
 class ParallelConfig:
     world_size: int = 1
@@ -152,11 +160,10 @@ def initialize_parallel_state(cfg: ParallelConfig) -> ParallelState:
     st.dp, _ = _make(dp_groups(W, tp), rank)
     st.ep, _ = _make(ep_groups(W, cfg.expert_parallel_size or W), rank)
     if cfg.decode_context_parallel_size > 1:
-        kv_all, _ = [], []
+        sets = []
         for g in tp_groups(W, tp):
-            kv, _h = dcp_groups(g, cfg.decode_context_parallel_size)
-            kv_all.extend(kv)
-        st.dcp, _ = _make(kv_all, rank)
+            sets.extend(dcp_decode_groups(g, cfg.decode_context_parallel_size))
+        st.dcp, _ = _make(sets, rank)
     st.cpu = dist.new_group(list(range(W)), backend="gloo")
     if W // tp > 1:
         for g in dp_groups(W, tp):

@@ -32,6 +32,17 @@ def _round(n: int) -> int:
     return (n + _ALIGN - 1) // _ALIGN * _ALIGN
 
 
+def dcp_slots(positions: np.ndarray, vblocks: np.ndarray, block_size: int, dcp_size: int,
+              dcp_rank: int) -> np.ndarray:
+    """KV-write slots of one DCP rank: scheduler blocks hold ``dcp_size * block_size`` tokens
+    and every rank keeps its ``block_size`` slice of each in its own cache block of the same id;
+    positions owned by another rank get -1 (no write).  ``vblocks``: the scheduler block of each
+    position (reference: CP-aware slot mapping, docs/design/parallelism/dcp.md)."""
+    off = positions % (block_size * dcp_size)
+    own = (off // block_size) == dcp_rank
+    return np.where(own, vblocks * block_size + off % block_size, -1).astype(np.int32)
+
+
 @dataclass
 class Layout:
     """Section offsets (int32 elements) inside the packed input buffer."""
@@ -46,7 +57,7 @@ class Layout:
         o = 0
         self.off = {}
         for name, n in (("ids", self.T), ("pos", self.T), ("slot", self.T), ("qstart", self.B + 1),
-                        ("seqlen", self.B), ("lidx", self.S), ("work", 2 * self.W),
+                        ("seqlen", self.B), ("lseqlen", self.B), ("lidx", self.S), ("work", 2 * self.W),
                         ("bt", self.B * self.nblk), ("temp", self.S), ("topk", self.S),
                         ("topp", self.S), ("minp", self.S), ("seed", 2 * self.S), ("offs", self.S),
                         ("rslot", self.S), ("sslot", self.B), ("nsplit", 1)):
@@ -70,6 +81,9 @@ class ModelRunner:
         self.max_model_len = max_model_len
         self.block_size = block_size
         self.max_blocks = (max_model_len + block_size - 1) // block_size
+        # Decode context parallelism: scheduler blocks of block_size tokens, of which this rank
+        # keeps the dcp_rank-th slice of cache_block_size tokens (see set_dcp)
+        self.dcp_size, self.dcp_rank, self.cache_block_size = 1, 0, block_size
         self.use_graphs = cuda_graphs and self.is_cuda and not envs.VLLM_B200_DISABLE_CUDA_GRAPHS
         cap = min(max_num_seqs, model.max_decode_tokens)
         self.graph_buckets = sorted(b for b in (graph_buckets or [1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128])
@@ -114,9 +128,23 @@ class ModelRunner:
         self.snapshot_max = envs.VLLM_B200_SNAPSHOT_MAX_STEPS
         self._snap_n = 0
 
+    def set_dcp(self, size: int, rank: int):
+        """Shard every sequence's KV over a DCP replica set of ``size`` ranks: the scheduler's
+        blocks (``self.block_size`` tokens) are split into ``size`` slices of the model's cache
+        block, and this rank writes and attends over slice ``rank`` only."""
+        if self.block_size % size:
+            raise ValueError("the scheduler block size must be a multiple of the DCP size")
+        self.dcp_size, self.dcp_rank = int(size), int(rank)
+        self.cache_block_size = self.block_size // size
+        self.use_graphs = False  # DCP steps run eagerly (their collectives are not captured)
+
+    def _group(self) -> int:
+        """Packed query rows per KV head: the local heads, times the DCP set (Q is gathered)."""
+        return max(1, self.model.Hq // self.model.Hkv) * self.dcp_size
+
     def _max_work(self) -> int:
         # prefill work items: ceil(q_len * G / 64) per sequence, bounded by tokens*G/64 + seqs
-        G = max(1, self.model.Hq // self.model.Hkv)
+        G = self._group()
         return self.max_tokens * G // ops.attention.PREFILL_ROWS + self.max_num_seqs + 1
 
     # ------------------------------------------------------------------ KV cache
@@ -165,6 +193,8 @@ class ModelRunner:
         slot = h[o["slot"][0]:o["slot"][0] + lay.T]
         qst = h[o["qstart"][0]:o["qstart"][0] + Bp + 1]
         sl = h[o["seqlen"][0]:o["seqlen"][0] + Bp]
+        lsl = h[o["lseqlen"][0]:o["lseqlen"][0] + Bp]
+        dcp = self.dcp_size
         bt = h[o["bt"][0]:o["bt"][0] + Bp * lay.nblk].reshape(Bp, lay.nblk)
         lidx = h[o["lidx"][0]:o["lidx"][0] + lay.S]
         t = 0
@@ -208,7 +238,12 @@ class ModelRunner:
                 P_mm = mm.positions3.shape[1]
                 pos[t:t + n] = np.where(p < P_mm, mm.positions3[0, np.minimum(p, P_mm - 1)], p + mm.delta)
             blocks = np.asarray(req.block_ids, dtype=np.int32)
-            slot[t:t + n] = blocks[p // bs] * bs + (p % bs)
+            if dcp > 1:
+                cbs = self.cache_block_size
+                slot[t:t + n] = dcp_slots(p, blocks[p // bs], cbs, dcp, self.dcp_rank)
+                lsl[i] = ops.dcp_local_count(st + n, cbs, dcp, self.dcp_rank)
+            else:
+                slot[t:t + n] = blocks[p // bs] * bs + (p % bs)
             qst[i] = t
             sl[i] = st + n
             q_lens[i] = n
@@ -236,6 +271,7 @@ class ModelRunner:
             slot[t] = -1
             qst[i] = t
             sl[i] = 1
+            lsl[i] = 1 if self.dcp_rank == 0 else 0
             q_lens[i] = 1
             bt[i, :] = 0
             sslot[i] = self.pad_slot
@@ -250,7 +286,7 @@ class ModelRunner:
             t += 1
             s += 1
         qst[Bp] = t
-        G = max(1, m.Hq // m.Hkv)
+        G = self._group()
         if pad_B is not None:
             w = ops.build_work(np.ones(Bp, dtype=np.int64), np.full(Bp, self.max_model_len), G, m.Hkv, self.num_sms,
                                max_splits=m.attn_splits_max, head_dim=m.D)
@@ -259,7 +295,8 @@ class ModelRunner:
                                   self.num_sms, max_splits=m.attn_splits_max, head_dim=m.D)
             h[o["nsplit"][0]] = min(real.num_splits, w.num_splits)
         else:
-            w = ops.build_work(q_lens[:Bp], sl[:Bp].astype(np.int64), G, m.Hkv, self.num_sms,
+            kv_lens = (lsl if dcp > 1 else sl)[:Bp].astype(np.int64)
+            w = ops.build_work(q_lens[:Bp], kv_lens, G, m.Hkv, self.num_sms,
                                max_splits=m.attn_splits_max, head_dim=m.D)
             h[o["nsplit"][0]] = w.num_splits
         work = h[o["work"][0]:o["work"][0] + 2 * len(w.work)]
@@ -360,6 +397,8 @@ class ModelRunner:
         fb.max_q_len = 1 if decode else getattr(self, "_last_max_q", 0)
         fb.splits_dev = sec("nsplit", 1) if decode and buf.is_cuda else None
         fb.seq_slots = sec("sslot", B)
+        if self.dcp_size > 1:
+            fb.seq_lens_local = sec("lseqlen", B)
         samp = dict(temperature=sec("temp", S, torch.float32), top_k=sec("topk", S),
                     top_p=sec("topp", S, torch.float32), min_p=sec("minp", S, torch.float32),
                     seeds=sec("seed", 2 * S).view(torch.int64), offsets=sec("offs", S),
@@ -499,13 +538,14 @@ class ModelRunner:
         vllm_neuron/vllm/worker/neuron_model_runner.py:7710)."""
         m = self.model
         lay = Layout(1, 1, 1, 1, self.max_blocks)
-        G = max(1, m.Hq // m.Hkv)
+        G = self._group()
         w = ops.build_work(np.ones(1, dtype=np.int64), np.ones(1, dtype=np.int64), G, m.Hkv,
                            self.num_sms, max_splits=1, head_dim=m.D)
         h = torch.zeros(lay.total, dtype=torch.int32)
         o = lay.off
         h[o["qstart"][0]:o["qstart"][0] + 2] = torch.arange(2, dtype=torch.int32)
         h[o["seqlen"][0]] = 1
+        h[o["lseqlen"][0]] = 1 if self.dcp_rank == 0 else 0
         h[o["slot"][0]] = -1
         h[o["work"][0]:o["work"][0] + 2 * len(w.work)] = torch.from_numpy(w.work.reshape(-1))
         h[o["topp"][0]] = torch.tensor([1.0]).view(torch.int32)
@@ -618,8 +658,7 @@ class ModelRunner:
         return self.launch(out, want_logprobs).result()
 
     def _max_work_for(self, out: SchedulerOutput) -> int:
-        m = self.model
-        G = max(1, m.Hq // m.Hkv)
+        G = self._group()
         return sum(math.ceil(s.num_tokens * G / ops.attention.PREFILL_ROWS) for s in out.scheduled) + 1
 
 
