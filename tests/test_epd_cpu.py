@@ -83,7 +83,7 @@ def test_encoder_disaggregation_matches_single_engine():
     assert encoder_calls == 0  # the serving instance never ran its vision encoder
 
 
-def _vision_dp_worker(rank, port, ckpt, q):
+def _vision_dp_worker(rank, port, ckpt, q, extra=None):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE="2",
                       LOCAL_RANK=str(rank))
     import torch
@@ -94,7 +94,7 @@ def _vision_dp_worker(rank, port, ckpt, q):
     from vllm_neuron_b200.parallel import state as ps
 
     try:
-        llm = LLM(ckpt, tensor_parallel_size=2, **KW)
+        llm = LLM(ckpt, tensor_parallel_size=2, **dict(KW, **(extra or {})))
         outs = llm.generate(_three_image_prompts(), SamplingParams(temperature=0, max_tokens=5, ignore_eos=True))
         q.put((rank, ([o.outputs[0].token_ids for o in outs], llm.engine.model.vision_calls)))
     except Exception:  # pragma: no cover
@@ -136,3 +136,30 @@ def test_vision_data_parallel_over_tp_ranks():
         assert not isinstance(res[r], str), res[r]
     assert res[0][0] == ref and res[1][0] == ref, (res, ref)
     assert res[0][1] == 2 and res[1][1] == 1
+
+
+def test_vision_tensor_parallel_over_tp_ranks():
+    """Vision TP=2 on TP=2: each rank holds half of every encoder block's heads and MLP
+    (all-reduced row-parallel projections); both ranks encode all three images together and
+    the tokens equal the TP=1 run."""
+    from vllm_neuron_b200.engine.sampling_params import SamplingParams
+    from vllm_neuron_b200.entrypoints import LLM
+
+    d, _ = _ckpt()
+    ref = LLM(d, **KW).generate(_three_image_prompts(),
+                                SamplingParams(temperature=0, max_tokens=5, ignore_eos=True))
+    ref = [o.outputs[0].token_ids for o in ref]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    extra = {"additional_config": {"neuron_config": {"vision_tp_size": 2}}}
+    procs = [ctx.Process(target=_vision_dp_worker, args=(r, port, d, q, extra)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    for r in (0, 1):
+        assert not isinstance(res[r], str), res[r]
+    assert res[0][0] == ref and res[1][0] == ref, (res, ref)
+    assert res[0][1] == 3 and res[1][1] == 3

@@ -191,6 +191,7 @@ class B200Config:
     fused_comm: bool = True           # fused GEMM+collective kernels (else NCCL baseline)
     use_cublas_baseline: bool = False  # library GEMMs instead of the tcgen05 kernels
     sampling_dp: bool = False          # TP decode: each rank samples 1/W of the rows (all-to-all)
+    vision_tp_size: int = 1            # vision encoder sharded over this many consecutive TP ranks
     extra: dict = field(default_factory=dict)
 
     @classmethod
@@ -223,7 +224,8 @@ class B200Config:
         return cls.from_dict(d)
 
     def validate(self):
-        for name in ("attention_dp_size", "embedding_dp_size", "lm_head_dp_size", "mlp_dp_size"):
+        for name in ("attention_dp_size", "embedding_dp_size", "lm_head_dp_size", "mlp_dp_size",
+                     "vision_tp_size"):
             v = getattr(self, name)
             if not isinstance(v, int) or v < 1:
                 raise ValueError(f"{name} must be a positive integer, got {v!r}")

@@ -96,6 +96,14 @@ def build_model(args: EngineArgs, tp: GroupComm = SINGLE):
     max_tok = max(args.max_num_batched_tokens, args.max_num_seqs)
     model = cls(arch, tp=tp, device=device, dtype=dtype, max_tokens=max_tok,
                 max_seqs=args.max_num_seqs, block_size=args.block_size)
+    if b200_config.vision_tp_size > 1 and hasattr(model, "set_vision_tp"):
+        from ..parallel import state as _ps
+
+        vt = _ps.get_parallel_state().vision_tp
+        if vt.world != b200_config.vision_tp_size:
+            raise ValueError("the parallel state has no vision TP group of this size "
+                             "(pass the option to the LLM front end)")
+        model.set_vision_tp(vt)
     if args.load_format == "dummy" or model_path is None:
         model.init_random(seed=args.seed)
     else:

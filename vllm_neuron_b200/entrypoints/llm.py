@@ -42,6 +42,11 @@ def _normalize_prompt(p: Any, tokenizer) -> list[int]:
     return [int(x) for x in p]
 
 
+def _b200_opts(additional_config: dict | None) -> dict:
+    a = additional_config or {}
+    return a.get("neuron_config") or a.get("b200_config") or {}
+
+
 class LLM:
     def __init__(self, model, tensor_parallel_size: int = 1, max_num_seqs: int = 256,
                  max_model_len: int | None = None, max_num_batched_tokens: int = 8192,
@@ -68,7 +73,8 @@ class LLM:
         st = ps.initialize_parallel_state(ps.ParallelConfig(world_size=world,
                                                             tensor_parallel_size=tensor_parallel_size,
                                                             data_parallel_size=dp,
-                                                            decode_context_parallel_size=decode_context_parallel_size))
+                                                            decode_context_parallel_size=decode_context_parallel_size,
+                                                            vision_tp_size=int(_b200_opts(additional_config).get("vision_tp_size", 1))))
         # Data parallelism: each group of TP ranks is an independent engine replica serving
         # every dp-th request; outputs are gathered over the DP group (reference: data
         # parallel replicas, docs/design/parallelism/data_parallelism.md).

@@ -33,6 +33,7 @@ import torch
 import torch.nn.functional as F
 
 from ..ops import linear as L
+from ..parallel.comm import SINGLE, GroupComm
 from .llama import LlamaForCausalLM
 
 
@@ -45,8 +46,17 @@ def _lin(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None) -> torch.Tens
 
 
 class Qwen3VLVision(torch.nn.Module):
-    def __init__(self, vc: dict, device, dtype):
+    """Qwen3-VL vision encoder.  With a vision TP group of ``V`` ranks each block's attention
+    heads and MLP are sharded (qkv / fc1 by output rows, proj / fc2 by input columns, followed
+    by an all-reduce; reference: the vision TP group, vllm_neuron/parallel/
+    neuron_parallel_state.py:667-701, model/qwen3_vl/vision_encoder_bf16.py:156,355,623)."""
+
+    SHARD_ROWS = ("qkv_w", "qkv_b", "fc1_w", "fc1_b")   # output-sharded block parameters
+    SHARD_COLS = ("proj_w", "fc2_w")                    # input-sharded block parameters
+
+    def __init__(self, vc: dict, device, dtype, tp: GroupComm = SINGLE):
         super().__init__()
+        self.tp = tp
         self.hidden = vc["hidden_size"]
         self.heads = vc["num_heads"]
         self.depth = vc["depth"]
@@ -61,6 +71,12 @@ class Qwen3VLVision(torch.nn.Module):
         self.deep_idx = list(vc.get("deepstack_visual_indexes") or [])
         self.act = vc.get("hidden_act", "gelu_pytorch_tanh")
         h, hm = self.hidden, self.hidden * self.merge ** 2
+        V = tp.world
+        if self.heads % V or self.inter % V:
+            raise ValueError(f"vision TP={V} must divide the vision heads ({self.heads}) and "
+                             f"the MLP width ({self.inter})")
+        self.heads_l, self.inter_l = self.heads // V, self.inter // V
+        hl = h // V
         kw = dict(device=device, dtype=dtype)
 
         def P(*shape):
@@ -73,10 +89,10 @@ class Qwen3VLVision(torch.nn.Module):
         for _ in range(self.depth):
             m = torch.nn.Module()
             m.n1_w, m.n1_b, m.n2_w, m.n2_b = P(h), P(h), P(h), P(h)
-            m.qkv_w, m.qkv_b = P(3 * h, h), P(3 * h)
-            m.proj_w, m.proj_b = P(h, h), P(h)
-            m.fc1_w, m.fc1_b = P(self.inter, h), P(self.inter)
-            m.fc2_w, m.fc2_b = P(h, self.inter), P(h)
+            m.qkv_w, m.qkv_b = P(3 * hl, h), P(3 * hl)
+            m.proj_w, m.proj_b = P(h, hl), P(h)
+            m.fc1_w, m.fc1_b = P(self.inter_l, h), P(self.inter_l)
+            m.fc2_w, m.fc2_b = P(h, self.inter_l), P(h)
             self.blocks.append(m)
 
         def merger(post_norm: bool):
@@ -91,6 +107,42 @@ class Qwen3VLVision(torch.nn.Module):
         self.deep_mergers = torch.nn.ModuleList([merger(True) for _ in self.deep_idx])
         hd = h // self.heads
         self.rot_inv_freq = 1.0 / (10000.0 ** (torch.arange(0, hd // 2, 2, dtype=torch.float32) / (hd // 2)))
+
+    def shard(self, name: str, full: torch.Tensor) -> torch.Tensor:
+        """This rank's slice of the unsharded block parameter ``full`` (``name`` ends with the
+        attribute name): q / k / v rows of the local heads, local MLP rows, or the matching
+        input columns of proj / fc2."""
+        V, r = self.tp.world, self.tp.rank
+        attr = name.rsplit(".", 1)[-1]
+        if V == 1 or (attr not in self.SHARD_ROWS and attr not in self.SHARD_COLS):
+            return full
+        if attr.startswith("qkv"):
+            h = self.hidden
+            hl = h // V
+            return full.view(3, h, *full.shape[1:])[:, r * hl:(r + 1) * hl].reshape(3 * hl, *full.shape[1:])
+        if attr in self.SHARD_ROWS:
+            n = full.shape[0] // V
+            return full[r * n:(r + 1) * n]
+        n = full.shape[1] // V
+        return full[:, r * n:(r + 1) * n]
+
+    def full_shape(self, name: str, local: torch.Tensor) -> tuple:
+        attr = name.rsplit(".", 1)[-1]
+        V = self.tp.world
+        if attr in self.SHARD_ROWS:
+            return (local.shape[0] * V,) + tuple(local.shape[1:])
+        if attr in self.SHARD_COLS:
+            return (local.shape[0], local.shape[1] * V)
+        return tuple(local.shape)
+
+    def _row_parallel(self, y: torch.Tensor, w: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+        """``y @ w.T + b`` with ``w`` sharded by input columns: partial sums all-reduced over
+        the vision TP group, the bias added once."""
+        if self.tp.world == 1:
+            return _lin(y, w, b)
+        part = _lin(y, w, None)
+        self.tp.all_reduce_(part)
+        return part + b
 
     # ---------------------------------------------------------------- position helpers
     def _pos_embed(self, grids: list[tuple[int, int, int]]) -> torch.Tensor:
@@ -154,8 +206,9 @@ class Qwen3VLVision(torch.nn.Module):
         x = x + self._pos_embed(grids)
         cos, sin = self._rotary(grids)
         lens = [t * h * w for t, h, w in grids]
-        H, nh = self.hidden, self.heads
-        hd = H // nh
+        H, nh = self.hidden, self.heads_l
+        hd = H // self.heads
+        Hl = nh * hd
         deep = []
         for li, blk in enumerate(self.blocks):
             y = F.layer_norm(x.float(), (H,), blk.n1_w.float(), blk.n1_b.float(), 1e-6).to(dt)
@@ -169,12 +222,12 @@ class Qwen3VLVision(torch.nn.Module):
             o0 = 0
             for n in lens:  # full attention inside each image
                 qi, ki, vi = (z[o0:o0 + n].transpose(0, 1)[None] for z in (q, k, v))
-                outs.append(F.scaled_dot_product_attention(qi, ki, vi)[0].transpose(0, 1).reshape(n, H))
+                outs.append(F.scaled_dot_product_attention(qi, ki, vi)[0].transpose(0, 1).reshape(n, Hl))
                 o0 += n
-            x = x + _lin(torch.cat(outs), blk.proj_w, blk.proj_b)
+            x = x + self._row_parallel(torch.cat(outs), blk.proj_w, blk.proj_b)
             y = F.layer_norm(x.float(), (H,), blk.n2_w.float(), blk.n2_b.float(), 1e-6).to(dt)
             y = self._act(_lin(y, blk.fc1_w, blk.fc1_b).float()).to(dt)
-            x = x + _lin(y, blk.fc2_w, blk.fc2_b)
+            x = x + self._row_parallel(y, blk.fc2_w, blk.fc2_b)
             if li in self.deep_idx:
                 deep.append(self._merge(self.deep_mergers[self.deep_idx.index(li)], x))
         emb = self._merge(self.merger, x)
@@ -222,6 +275,7 @@ class Qwen3VLForConditionalGeneration(LlamaForCausalLM):
         raw = cfg.raw
         vc = dict(raw.get("vision_config") or {})
         vc.setdefault("out_hidden_size", self.H)
+        self.visual_config = vc
         self.visual = Qwen3VLVision(vc, self.device, self.dtype)
         rp = (raw.get("rope_parameters") or raw.get("rope_scaling") or {})
         sec = rp.get("mrope_section") or [24, 20, 20]
@@ -240,8 +294,16 @@ class Qwen3VLForConditionalGeneration(LlamaForCausalLM):
                 prm.fill_(1.0)
             elif name.endswith("_b"):
                 prm.zero_()
-            else:
-                prm.normal_(0.0, std, generator=g)
+            else:  # drawn at full size, then sharded: the same weights for every vision TP size
+                full = torch.empty(self.visual.full_shape(name, prm), dtype=prm.dtype, device=prm.device)
+                full.normal_(0.0, std, generator=g)
+                prm.copy_(self.visual.shard(name, full))
+
+    def set_vision_tp(self, group: GroupComm):
+        """Rebuild the (not yet loaded) vision encoder sharded over ``group``: consecutive TP
+        ranks; the TP group then holds TP / V vision-DP replicas."""
+        vc = self.visual_config
+        self.visual = Qwen3VLVision(vc, self.device, self.dtype, tp=group)
 
     vision_dp = True  # split a request's images over the TP ranks (vision data parallelism)
     vision_calls = 0  # images encoded by this rank (observability / tests)
@@ -255,16 +317,18 @@ class Qwen3VLForConditionalGeneration(LlamaForCausalLM):
         (padded to the largest share), instead of every rank encoding every image.  Reference:
         the vision TP/DP groups (vllm_neuron/parallel/neuron_parallel_state.py:667-701; vision
         DP defaults to the world, vllm_neuron/model/neuron_config.py:345-404)."""
-        W = self.tp.world
+        V = self.visual.tp.world
+        W = self.tp.world // V   # vision-DP replicas of V consecutive ranks
         if W == 1 or len(grids) < 2 or not self.vision_dp:
             self.vision_calls += len(grids)
             return self.visual(pixels, grids)
+        replica = self.tp.rank // V
         m2 = self.spatial_merge ** 2
         counts = [t * h * w for t, h, w in grids]
         starts = [sum(counts[:i]) for i in range(len(grids))]
         rows = [c // m2 for c in counts]
         owner = [i % W for i in range(len(grids))]
-        mine = [i for i in range(len(grids)) if owner[i] == self.tp.rank]
+        mine = [i for i in range(len(grids)) if owner[i] == replica]
         H = self.H
         if mine:
             px = torch.cat([pixels[starts[i]:starts[i] + counts[i]] for i in mine])
@@ -280,12 +344,12 @@ class Qwen3VLForConditionalGeneration(LlamaForCausalLM):
         pack[:n, :H] = emb
         if nd:
             pack[:n, H:] = deep.permute(1, 0, 2).reshape(n, nd * H).to(emb.dtype)
-        allp = self.tp.all_gather(pack.unsqueeze(0), dim=0)          # [W, R, H * (1 + nd)]
+        allp = self.tp.all_gather(pack.unsqueeze(0), dim=0)  # [W * V, R, H * (1 + nd)]
         offs = [0] * W
         e_parts, d_parts = [], []
         for i in range(len(grids)):
             r = owner[i]
-            blk = allp[r, offs[r]:offs[r] + rows[i]]
+            blk = allp[r * V, offs[r]:offs[r] + rows[i]]  # the replica's first rank
             offs[r] += rows[i]
             e_parts.append(blk[:, :H])
             if nd:

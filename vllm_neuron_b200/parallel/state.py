@@ -91,6 +91,8 @@ class ParallelConfig:
             raise ValueError("world_size must equal TP x DP")
         if self.tensor_parallel_size % self.decode_context_parallel_size:
             raise ValueError("DCP size must divide TP")
+        if self.tensor_parallel_size % self.vision_tp_size:
+            raise ValueError("vision_tp_size must divide TP")
         if self.tensor_parallel_size % self.attention_dp_size:
             raise ValueError("attention_dp_size must divide TP")
         ep = self.expert_parallel_size or self.world_size
@@ -106,6 +108,7 @@ class ParallelState:
     dp: GroupComm = field(default_factory=lambda: GroupComm(None))
     ep: GroupComm = field(default_factory=lambda: GroupComm(None))
     dcp: GroupComm = field(default_factory=lambda: GroupComm(None))
+    vision_tp: GroupComm = field(default_factory=lambda: GroupComm(None))
     cpu: dist.ProcessGroup | None = None
     dp_cpu: dist.ProcessGroup | None = None   # gloo group of this rank's DP peers
     groups: dict = field(default_factory=dict)
@@ -164,6 +167,11 @@ def initialize_parallel_state(cfg: ParallelConfig) -> ParallelState:
         for g in tp_groups(W, tp):
             sets.extend(dcp_decode_groups(g, cfg.decode_context_parallel_size))
         st.dcp, _ = _make(sets, rank)
+    if cfg.vision_tp_size > 1:  # vision encoder TP: consecutive ranks of each TP group
+        sets = []
+        for g in tp_groups(W, tp):
+            sets.extend(sub_groups(g, cfg.vision_tp_size)[0])
+        st.vision_tp, _ = _make(sets, rank)
     st.cpu = dist.new_group(list(range(W)), backend="gloo")
     if W // tp > 1:
         for g in dp_groups(W, tp):

@@ -12,6 +12,8 @@ fused_qkv_weight_loader with KV replication, padding loaders).
 """
 from __future__ import annotations
 
+import collections
+
 from typing import Callable
 
 import torch
@@ -229,10 +231,17 @@ def load_qwen3_5(model, get_tensor: Callable[[str], torch.Tensor], names: set[st
     _copy(model.lm_head, shard_rows(get_tensor("lm_head.weight"), W, r, model.V_local), "lm_head")
 
 
+_VIS_ATTR = {"attn.qkv.weight": "qkv_w", "attn.qkv.bias": "qkv_b", "attn.proj.weight": "proj_w",
+             "mlp.linear_fc1.weight": "fc1_w", "mlp.linear_fc1.bias": "fc1_b",
+             "mlp.linear_fc2.weight": "fc2_w"}
+_VIS_ATTR = collections.defaultdict(lambda: "replicated", _VIS_ATTR)
+
+
 @torch.no_grad()
 def load_qwen3_vl_vision(vis, get_tensor: Callable[[str], torch.Tensor], names: set[str]):
-    """Qwen3-VL vision encoder (replicated on every rank): Conv3d patch embedding flattened to
-    a linear layer, position table, blocks, merger and DeepStack mergers."""
+    """Qwen3-VL vision encoder: Conv3d patch embedding flattened to a linear layer, position
+    table, blocks (attention heads and MLP sharded over the vision TP group, if any), merger
+    and DeepStack mergers (replicated)."""
     pre = "model.visual." if any(n.startswith("model.visual.") for n in names) else "visual."
     w = get_tensor(pre + "patch_embed.proj.weight")
     _copy(vis.patch_w, w.reshape(w.shape[0], -1), "patch_embed")
@@ -245,7 +254,7 @@ def load_qwen3_vl_vision(vis, get_tensor: Callable[[str], torch.Tensor], names: 
                          (blk.proj_w, "attn.proj.weight"), (blk.proj_b, "attn.proj.bias"),
                          (blk.fc1_w, "mlp.linear_fc1.weight"), (blk.fc1_b, "mlp.linear_fc1.bias"),
                          (blk.fc2_w, "mlp.linear_fc2.weight"), (blk.fc2_b, "mlp.linear_fc2.bias")):
-            _copy(dst, get_tensor(p + src), p + src)
+            _copy(dst, vis.shard(p + _VIS_ATTR[src], get_tensor(p + src)), p + src)
     mergers = [(vis.merger, pre + "merger.")] + [(m, f"{pre}deepstack_merger_list.{j}.")
                                                    for j, m in enumerate(vis.deep_mergers)]
     for m, p in mergers:
