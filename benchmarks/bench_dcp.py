@@ -7,11 +7,14 @@ Communication (the Q all-gather and the partial all-to-all) is not included.
 """
 import argparse
 import json
+import os
+import sys
 
 import numpy as np
 import torch
 
-from vllm_neuron_b200 import ops
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+from vllm_neuron_b200 import ops  # noqa: E402
 
 
 def _time(fn, iters=20, warmup=3):
