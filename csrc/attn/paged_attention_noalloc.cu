@@ -12,6 +12,7 @@
 #include <stdio.h>
 
 #include <atomic>
+#include <exception>
 #include <mutex>
 
 #include "attention.h"
@@ -139,6 +140,8 @@ extern "C" __attribute__((visibility("default"))) int b200_paged_attention_noall
   try {
     b200::paged_attention_launch(p, num_work, head_dim, decode != 0,
                                  reinterpret_cast<cudaStream_t>(stream));
+  } catch (const std::exception& e) {
+    return fail(err, err_len, B200_NOALLOC_ERR_INVALID, "launch rejected the arguments: %s", e.what());
   } catch (...) {
     return fail(err, err_len, B200_NOALLOC_ERR_INVALID, "launch rejected the arguments");
   }

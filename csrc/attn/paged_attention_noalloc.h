@@ -14,8 +14,11 @@
 // library's own device memory instead, so it calls no cudaMalloc, cudaFree or allocating
 // library routine.
 //
-// Limit.  The scratch array holds B200_NOALLOC_SCRATCH_BYTES (16 MiB) on every GPU that
-// loads the library, until the process exits.  A call needs
+// Limit.  The scratch array is B200_NOALLOC_SCRATCH_BYTES (16 MiB) of device memory.  With
+// CUDA's lazy module loading it is reserved on a device when the library's module is first
+// loaded there (at the library's first kernel launch on that device, or at the first call of
+// this entry point, whose set-up can itself trigger that load) and stays reserved until the
+// process exits.  A call needs
 //   4 * num_splits * total_tokens * num_q_heads * (head_dim + 1) bytes
 // (plus at most 256 bytes of alignment padding) when num_splits > 1, and none otherwise;
 // larger calls are rejected with B200_NOALLOC_ERR_TOO_LARGE and a message.
@@ -27,8 +30,9 @@
 // and produce wrong results.
 //
 // Set-up.  The first call on a device, with that device current, looks up the device
-// address of the array (cudaGetSymbolAddress) and caches it; later calls reuse it.  Make
-// that first call before any stream capture starts on the device.
+// address of the array (cudaGetSymbolAddress) and caches it; later calls reuse it.  That
+// look-up may load the module on the device (see Limit), so make the first call before any
+// stream capture starts on the device.
 #pragma once
 
 #include <stddef.h>
@@ -51,8 +55,11 @@ extern "C" {
 // pointers of the current device; `work` is int32 [num_work, 2] (sequence, first packed
 // row) as built by vllm_neuron_b200.ops.attention.build_work, and block_tables / seq_lens /
 // q_start are int32 as for the Python op.  `sinks` is fp32 [num_q_heads] or NULL; `window`
-// is 0 for full attention; `decode` selects the 16-row decode tiling; head_dim is 64 or
-// 128.  `stream` is a cudaStream_t (NULL for the legacy default stream).  On failure the
+// is 0 for full attention; head_dim is 64 or 128.  `decode` selects the 16-row decode
+// tiling, which assumes one query token per sequence: pass 1 only when every step
+// q_start[i + 1] - q_start[i] is 1 (the `decode` flag that build_work returns), else 0 --
+// the entry point does not check it, and a multi-token query with decode = 1 gives wrong
+// results.  `stream` is a cudaStream_t (NULL for the legacy default stream).  On failure the
 // return code is non-zero and, when err is not NULL, a NUL-terminated message of at most
 // err_len bytes is written to it.
 int b200_paged_attention_noalloc(const void* q, long long q_stride_t, const void* k_cache,

@@ -1,8 +1,15 @@
-"""Tensor parallelism on real GPUs: TP=2 over NCCL must reproduce TP=1 logits.
+"""Tensor parallelism on real GPUs: TP=2 must reproduce TP=1 logits and tokens.
 
 Runs a small Llama (GPU-sized heads) from one HF checkpoint at TP=1 (in this process) and
-TP=2 (two torchrun ranks), comparing the greedy tokens of a short generation and the first
-step's logits.  Skipped unless two CUDA devices are visible.
+TP=2 (two torchrun ranks) with NCCL collectives, the fused decode all-reduce, sequence
+parallelism (NCCL and fused) and sampling data parallelism.  It compares
+
+* the last-position logits of a prefill step of 6 x 40 tokens (the prefill path: SP when on)
+  and of 6 x 16 tokens (96 rows: the decode-regime GEMMs and the fused all-reduce), relative
+  error below 2e-2 and the same argmax, and
+* the greedy tokens of a short generation whose decode batch shrinks as requests finish.
+
+Skipped unless two CUDA devices are visible.
 """
 import json
 import os
@@ -33,6 +40,8 @@ llm = LLM(ckpt, tensor_parallel_size=int(os.environ["WORLD_SIZE"]), max_num_seqs
                                              "sampling_dp": sdp}})
 g = torch.Generator().manual_seed(0)
 prompts = [torch.randint(0, 32000, (40,), generator=g).tolist() for _ in range(6)]
+lg_long = llm.engine.prompt_logits(prompts)
+lg_short = llm.engine.prompt_logits([p[:16] for p in prompts])
 sps = [SamplingParams(temperature=0, max_tokens=n, ignore_eos=True) for n in MAX_TOKENS]
 outs = llm.generate(prompts, sps)
 from vllm_neuron_b200.ops._ext import ext
@@ -44,6 +53,7 @@ spf = llm.engine.model.sp_fused
 assert not (fused and sp) or (spf is not None and spf.forwards > 0), "fused SP collectives did not run"
 if int(os.environ["RANK"]) == 0:
     json.dump([o.outputs[0].token_ids for o in outs], open(out_path, "w"))
+    torch.save({"long": lg_long, "short": lg_short}, out_path + ".pt")
 llm.shutdown()
 import torch.distributed as dist
 dist.barrier(); dist.destroy_process_group()
@@ -82,7 +92,7 @@ def _run_tp(ckpt, world, fused, sp=False, sdp=False):
            "--master-addr=127.0.0.1", f"--master-port={_port()}", script, ROOT, ckpt, out, "1" if fused else "0", "1" if sp else "0", "1" if sdp else "0"]
     r = subprocess.run(["timeout", "-k", "30", "300"] + cmd, env=env, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
-    return json.load(open(out))
+    return json.load(open(out)), torch.load(out + ".pt")
 
 
 @pytest.mark.parametrize("fused,sp,sdp", [(False, False, False), (True, False, False), (False, True, False),
@@ -96,10 +106,18 @@ def test_tp2_matches_tp1(ckpt, fused, sp, sdp):
     g = torch.Generator().manual_seed(0)
     prompts = [torch.randint(0, 32000, (40,), generator=g).tolist() for _ in range(6)]
     sps = [SamplingParams(temperature=0, max_tokens=n, ignore_eos=True) for n in [12, 5, 9, 12, 3, 7]]
-    ref = LLM(ckpt, max_num_seqs=8, max_model_len=256, num_gpu_blocks=256, max_num_batched_tokens=256,
-              skip_tokenizer_init=True).generate(prompts, sps)
-    ref = [o.outputs[0].token_ids for o in ref]
-    got = _run_tp(ckpt, 2, fused, sp, sdp)
+    llm = LLM(ckpt, max_num_seqs=8, max_model_len=256, num_gpu_blocks=256, max_num_batched_tokens=256,
+              skip_tokenizer_init=True)
+    ref_long = llm.engine.prompt_logits(prompts)
+    ref_short = llm.engine.prompt_logits([p[:16] for p in prompts])
+    ref = [o.outputs[0].token_ids for o in llm.generate(prompts, sps)]
+    llm.shutdown()
+    got, lg = _run_tp(ckpt, 2, fused, sp, sdp)
+    for name, r in (("long", ref_long), ("short", ref_short)):
+        t = lg[name]
+        rel = float((t - r).norm() / r.norm())
+        assert rel < 2e-2, (name, rel)
+        assert torch.equal(t.argmax(-1), r.argmax(-1)), name
     # bf16 reduction order differs between TP sizes: require the first tokens to agree and
     # most of the sequence to match.
     same = sum(a == b for r, g2 in zip(ref, got) for a, b in zip(r, g2))

@@ -38,17 +38,17 @@ def _lib():
     return fn
 
 
-def _batch(device, ctx_lens, Hq, Hkv, D, bs=16, seed=0):
+def _batch(device, ctx_lens, Hq, Hkv, D, bs=16, seed=0, q_lens=None):
     g = torch.Generator(device="cpu").manual_seed(seed)
     B = len(ctx_lens)
-    q_lens = [1] * B
-    seq_lens = [c + 1 for c in ctx_lens]
+    q_lens = list(q_lens) if q_lens is not None else [1] * B
+    seq_lens = [c + n for c, n in zip(ctx_lens, q_lens)]
     max_blocks = max((s + bs - 1) // bs for s in seq_lens)
     nb = B * max_blocks + 3
     bt = (torch.randperm(nb - 1, generator=g)[: B * max_blocks] + 1).view(B, max_blocks)
     kc = (torch.randn(nb, Hkv, bs, D, generator=g) * 0.5).to(torch.bfloat16).to(device)
     vc = torch.randn(nb, Hkv, bs, D, generator=g).to(torch.bfloat16).to(device)
-    q = torch.randn(B, Hq, D, generator=g).to(torch.bfloat16).to(device)
+    q = torch.randn(sum(q_lens), Hq, D, generator=g).to(torch.bfloat16).to(device)
     qs = torch.tensor([0] + list(np.cumsum(q_lens)), dtype=torch.int32, device=device)
     sl = torch.tensor(seq_lens, dtype=torch.int32, device=device)
     return q, kc, vc, bt.to(torch.int32).to(device), sl, qs, np.array(q_lens)
@@ -110,3 +110,34 @@ def test_noalloc_rejects_oversized_scratch(cuda_device):
     rc, msg, _ = _call(fn, q, kc, vc, bt, sl, qs, work, True, splits, 1 / math.sqrt(D))
     assert rc == ERR_TOO_LARGE
     assert "scratch" in msg
+
+
+def _check(fn, device, ctx, Hq, Hkv, D, splits=None, q_lens=None, seed=0):
+    q, kc, vc, bt, sl, qs, ql = _batch(device, ctx, Hq, Hkv, D, seed=seed, q_lens=q_lens)
+    w = ops.build_work(ql, sl.cpu().numpy(), Hq // Hkv, Hkv, head_dim=D)
+    splits = splits if splits is not None else w.num_splits
+    work = torch.from_numpy(w.work).to(device)
+    scale = 1 / math.sqrt(D)
+    ref = ops.paged_attention(q, kc, vc, bt, sl, qs, work, w.decode, splits, scale)
+    rc, msg, out = _call(fn, q, kc, vc, bt, sl, qs, work, w.decode, splits, scale)
+    torch.cuda.synchronize()
+    assert rc == 0, msg
+    assert _rel_err(out, ref) < 2e-2
+    assert _rel_err(out, ops.paged_attention_ref(q, kc, vc, bt, sl, qs, scale)) < 2e-2
+    return w
+
+
+def test_noalloc_leftovers_head_dim_64_and_prefill_tiling(cuda_device):
+    """Two calls with the same token count and split factor: the first fills every split of
+    the shared array, the second has contexts short enough that its upper splits hold no keys
+    and must overwrite the first call's partials with empty ones.  Then head_dim 64 and the
+    prefill (multi-token query) tiling, which needs no scratch."""
+    fn = _lib()
+    Hq, Hkv, D = 32, 8, 128
+    _check(fn, cuda_device, [4000, 3000, 3500, 2500, 3900, 3100, 2900, 3700], Hq, Hkv, D, splits=16, seed=3)
+    _check(fn, cuda_device, [5, 20, 1, 40, 9, 30, 2, 16], Hq, Hkv, D, splits=16, seed=4)
+    w = _check(fn, cuda_device, [700, 64, 1300, 9, 2000, 333], 16, 4, 64, splits=8, seed=5)
+    assert w.decode
+    w = _check(fn, cuda_device, [0, 100, 37], Hq, Hkv, D, q_lens=[50, 20, 90], seed=6)
+    assert not w.decode
+

@@ -118,6 +118,10 @@ def build_model(args: EngineArgs, tp: GroupComm = SINGLE):
             raise ValueError(f"{type(model).__name__} does not support kv_cache_dtype={args.kv_cache_dtype!r}")
         model.set_kv_cache_dtype(args.kv_cache_dtype, _kv_scales_from_checkpoint(model, model_path))
     real_group = tp.world > 1 and tp.group is not None
+    # same-box comparison build: dense projections on cuBLAS (and, with fused_comm off, NCCL)
+    from ..ops import linear as _lin
+
+    _lin.set_library_gemm(b200_config.use_cublas_baseline)
     if b200_config.sequence_parallel and hasattr(model, "sequence_parallel"):
         model.sequence_parallel = True
     if (real_group and device.type == "cuda" and b200_config.fused_comm

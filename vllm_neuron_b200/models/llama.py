@@ -512,9 +512,7 @@ class LlamaForCausalLM(torch.nn.Module):
         d = self.dcp
         T, Hq, D, ns, W = b.num_tokens, self.Hq, self.D, b.num_splits, self.dcp.world
         qg = d.all_gather(q.view(T, Hq, D), dim=1)  # [T, W * Hq, D], heads in rank order
-        dev = q.device
-        po = torch.empty((ns, T, W * Hq, D), dtype=torch.float32, device=dev)
-        pl = torch.empty((ns, T, W * Hq), dtype=torch.float32, device=dev)
+        po, pl = self._dcp_partials(ns, T, W * Hq, D, q.device)
         ops.paged_attention_partial(qg, k_cache, v_cache, b.block_tables, b.seq_lens_local,
                                     b.q_start, b.work, b.decode, ns, self.scale, po, pl,
                                     k_scale=kv_scale[0], v_scale=kv_scale[1],
@@ -524,6 +522,18 @@ class LlamaForCausalLM(torch.nn.Module):
         rl = d.all_to_all(pl.view(ns, T, W, Hq).permute(2, 0, 1, 3).contiguous())
         ops.attn_combine(ro.view(W * ns, T, Hq, D), rl.view(W * ns, T, Hq),
                          out=attn.view(T, Hq, D))
+
+    def _dcp_partials(self, ns: int, T: int, Hg: int, D: int, dev) -> tuple[torch.Tensor, torch.Tensor]:
+        """Views ``[ns, T, Hg, D]`` / ``[ns, T, Hg]`` of one fp32 workspace kept on the model and
+        grown (never shrunk) to the largest step seen: sized on the first decode step for the
+        decode bound and on the first prefill chunk for the token budget, not allocated per
+        layer."""
+        n_o, n_l = ns * T * Hg * D, ns * T * Hg
+        ws = getattr(self, "_dcp_ws", None)
+        if ws is None or ws.numel() < n_o + n_l:
+            cap = max(n_o + n_l, self.attn_splits_max * self.max_decode_tokens * Hg * (D + 1))
+            self._dcp_ws = ws = torch.empty(cap, dtype=torch.float32, device=dev)
+        return ws[:n_o].view(ns, T, Hg, D), ws[n_o:n_o + n_l].view(ns, T, Hg)
 
     def compute_logits(self, x: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:
         S = idx.shape[0]

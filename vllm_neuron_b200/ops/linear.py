@@ -104,6 +104,25 @@ def _fp8_ref(xq: torch.Tensor, w: FP8Weight) -> torch.Tensor:
 SKINNY_MAX = 128
 SILU_BLOCK = 128  # gate/up interleave block = BN/2 of the fused SwiGLU epilogue
 
+# Library-GEMM mode (``use_cublas_baseline``): the dense bf16 projections run on cuBLAS through
+# torch.mm instead of the tcgen05 kernels; everything else (attention, norms, RoPE, sampling)
+# stays on this framework's kernels.  This is the same-box NCCL + cuBLAS comparison build.
+_LIBRARY_GEMM = False
+
+
+def set_library_gemm(on: bool) -> None:
+    """Route the dense bf16 projections through cuBLAS (``True``) or the tcgen05 GEMM."""
+    global _LIBRARY_GEMM
+    _LIBRARY_GEMM = bool(on)
+
+
+def library_gemm() -> bool:
+    return _LIBRARY_GEMM
+
+
+def _lib(x: torch.Tensor, w) -> bool:
+    return _LIBRARY_GEMM and x.is_cuda and isinstance(w, torch.Tensor)
+
 _NUM_SMS: dict[int, int] = {}
 
 
@@ -162,6 +181,9 @@ def gemm_out(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,
     if not x.is_cuda:
         out.copy_((x.float() @ w.float().t()).to(out.dtype))
         return out
+    if _lib(x, w):
+        torch.mm(x, w.t(), out=out)
+        return out
     if bn is None:
         bn = _pick_bn_wide(M, N, num_sms(x.device))
     ext().gemm(x, w, out, EPI_BF16, bn, 1, 0, 0)
@@ -178,6 +200,9 @@ def gemm_skinny_bf16(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None 
         out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
     if not x.is_cuda:
         out.copy_((x.float() @ w.float().t()).to(out.dtype))
+        return out
+    if _lib(x, w):
+        torch.mm(x, w.t(), out=out)
         return out
     ext().gemm(w, x, out, EPI_BF16_T, skinny_bn(M), 1, 0, 0)
     return out
@@ -208,6 +233,10 @@ def gemm_accumulate(x: torch.Tensor, w: torch.Tensor, acc: torch.Tensor,
         return acc
     if not x.is_cuda:
         acc[:M].add_(x.float() @ w.float().t())
+        return acc
+    if _lib(x, w):
+        # acc is zero on entry: one cuBLAS call with an fp32 output (bf16 inputs)
+        torch.mm(x, w.t(), out_dtype=torch.float32, out=acc[:M])
         return acc
     # splits=None: split-K when the row tiles alone under-fill the SMs (measured faster for
     # the small qkv / o projections), stream-K (-1: every persistent CTA takes an equal share
@@ -243,6 +272,10 @@ def gemm_silu(x: torch.Tensor, w_gu: torch.Tensor, out: torch.Tensor | None = No
         y = x.float() @ w_gu.float().t()
         out.copy_(silu_mul_ref(y, SILU_BLOCK).to(out.dtype))
         return out
+    if _lib(x, w_gu):
+        from .activation import silu_mul
+
+        return silu_mul(torch.mm(x, w_gu.t()), out=out, blk=SILU_BLOCK)
     ext().gemm(x, w_gu, out, EPI_SILU_BF16, 2 * SILU_BLOCK, 1, 0, 0)
     return out
 
