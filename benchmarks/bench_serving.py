@@ -57,13 +57,13 @@ MODELS = {
              "layer_types": (["linear_attention"] * 3 + ["full_attention"]) * 10,
              "rope_parameters": {"rope_type": "default", "rope_theta": 10000000.0, "partial_rotary_factor": 0.25},
              "max_position_embeddings": 32768},
-        workload=(64, 4096, 256)),
+        workload=(64, 4096, 256), quant="fp8_block"),
     "llama3-70b": dict(
         cfg={"architectures": ["LlamaForCausalLM"], "model_type": "llama", "hidden_size": 8192,
              "num_hidden_layers": 80, "num_attention_heads": 64, "num_key_value_heads": 8, "head_dim": 128,
              "intermediate_size": 28672, "vocab_size": 128256, "rms_norm_eps": 1e-5, "rope_theta": 500000.0,
              "max_position_embeddings": 16384},
-        workload=(16, 8192, 512)),
+        workload=(16, 8192, 512), quant="fp8_block", mnbt=4096, sp=True),
 }
 
 
@@ -74,12 +74,16 @@ def main():
     ap.add_argument("--num-prompts", type=int, default=None)
     ap.add_argument("--input-len", type=int, default=None)
     ap.add_argument("--output-len", type=int, default=None)
-    ap.add_argument("--max-num-batched-tokens", type=int, default=8192)
+    ap.add_argument("--max-num-batched-tokens", type=int, default=None)
     ap.add_argument("--warmup-prompts", type=int, default=4)
     ap.add_argument("--json", default=None)
-    ap.add_argument("--quant", default=None, choices=[None, "fp8_static"],
-                    help="fp8_static: W8A8 FP8 projections (random weights quantized per tensor)")
+    ap.add_argument("--quant", default="auto", choices=["auto", "none", "fp8_static", "fp8_block"],
+                    help="fp8_static: W8A8 FP8 projections (random weights quantized per tensor); "
+                         "fp8_block: 128 x 128 block-scaled FP8 weights, bf16 activations; auto: the "
+                         "configuration's own (fp8_block for llama3-70b and qwen3.6-a3b)")
     ap.add_argument("--sp", action="store_true", help="sequence-parallel prefill (TP > 1)")
+    ap.add_argument("--baseline", action="store_true",
+                    help="NCCL + cuBLAS build of the same engine (no fused kernels, library GEMMs)")
     a = ap.parse_args()
 
     from vllm_neuron_b200.engine.sampling_params import SamplingParams
@@ -97,12 +101,16 @@ def main():
     max_len = IN + OUT + 16
     blocks = P * ((max_len + 15) // 16) + 64
     nc = {}
-    if a.quant:
-        nc["quantization"] = a.quant
-    if a.sp:
+    quant = m.get("quant") if a.quant == "auto" else (None if a.quant == "none" else a.quant)
+    if quant:
+        nc["quantization"] = quant
+    if a.sp or (m.get("sp") and world > 1):
         nc["sequence_parallel"] = True
+    if a.baseline:
+        nc.update(fused_comm=False, use_cublas_baseline=True)
+    mnbt = a.max_num_batched_tokens or m.get("mnbt", 8192)
     llm = LLM(dict(m["cfg"]), tensor_parallel_size=world, max_num_seqs=P, max_model_len=max_len,
-              max_num_batched_tokens=a.max_num_batched_tokens, load_format="dummy", num_gpu_blocks=blocks,
+              max_num_batched_tokens=mnbt, load_format="dummy", num_gpu_blocks=blocks,
               skip_tokenizer_init=True, seed=0, additional_config={"neuron_config": nc} if nc else None)
     vocab = m["cfg"]["vocab_size"]
     g = torch.Generator().manual_seed(7)
@@ -132,8 +140,11 @@ def main():
     res = {"model": a.model, "tp": world, "num_prompts": P, "input_len": IN, "output_len": OUT,
            "output_tok_s": P * OUT / (ms / 1e3), "wall_s": wall, "device_s": ms / 1e3,
            "p50_ttft_ms": float(np.median(ttft)) * 1e3, "p50_tpot_ms": float(np.median(tpot)) * 1e3,
-           "dtype": "bf16" + (" activations, fp8 W8A8 projections" if a.quant else ""),
-           "sp": bool(a.sp), "data": "synthetic prompts, random-init weights"}
+           "dtype": "bf16" + ({"fp8_static": " activations, fp8 W8A8 projections",
+                               "fp8_block": " activations, 128x128 block-scaled fp8 weights"}.get(quant, "")),
+           "sp": bool(nc.get("sequence_parallel")), "max_num_batched_tokens": mnbt,
+           "build": "nccl+cublas baseline" if a.baseline else "fused sm_100a",
+           "data": "synthetic prompts, random-init weights"}
     if rank == 0:
         print(json.dumps(res), flush=True)
         if a.json:

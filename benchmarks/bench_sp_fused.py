@@ -47,7 +47,7 @@ class _LocalSP:
         par = self.rs_calls % 2
         self.rs_calls += 1
         ext().gemm_sp(a, w, self.x[0, :1], 5, bn, 0, [], 0, [self.slots[par].data_ptr()],
-                      [self.ctr.data_ptr()], self.T)
+                      [self.ctr.data_ptr()], self.T, None)
         self.rs_target += -(-self.T // 128) * -(-w.shape[0] // bn)
 
     def norm_push(self, res, nw):
@@ -60,7 +60,8 @@ class _LocalSP:
         return self.x[par]
 
     def gemm_ag(self, x, w, out, bn):
-        ext().gemm_sp(x, w, out, L.EPI_BF16, bn, self.ctr.data_ptr() + 4, [self.ag_target], self.T, [], [], 0)
+        ext().gemm_sp(x, w, out, L.EPI_BF16, bn, self.ctr.data_ptr() + 4, [self.ag_target], self.T, [], [], 0,
+                      None)
 
 
 def _time(fn, iters, warmup):

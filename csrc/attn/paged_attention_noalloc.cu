@@ -141,7 +141,9 @@ extern "C" __attribute__((visibility("default"))) int b200_paged_attention_noall
     b200::paged_attention_launch(p, num_work, head_dim, decode != 0,
                                  reinterpret_cast<cudaStream_t>(stream));
   } catch (const std::exception& e) {
-    return fail(err, err_len, B200_NOALLOC_ERR_INVALID, "launch rejected the arguments: %s", e.what());
+    if (err != nullptr && err_len > 0)
+      snprintf(err, err_len, "launch rejected the arguments: %s", e.what());
+    return B200_NOALLOC_ERR_INVALID;
   } catch (...) {
     return fail(err, err_len, B200_NOALLOC_ERR_INVALID, "launch rejected the arguments");
   }

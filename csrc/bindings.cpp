@@ -110,6 +110,63 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, int64_t epi
 
 static void fill_ptrs(const std::vector<int64_t>& v, void** dst, const char* what);
 
+// Block-scaled FP8 weight GEMM (W8A16): out = a @ b^T where the weight operand (a when w8 == 1,
+// b when w8 == 2) is float8_e4m3fn with fp32 scales [ceil(rows / 128), ceil(K / 128)] and the
+// other operand is bf16; the kernel widens weight tiles in shared memory (gemm_sm100.cu).
+// gtiles / gcount select the grouped (MoE) mode with w8 == 2.
+void gemm_w8(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, int64_t epi, int64_t bn,
+             int64_t splits, const at::Tensor& scales, int64_t w8, c10::optional<at::Tensor> gtiles,
+             c10::optional<at::Tensor> gcount) {
+  CHECK_CUDA(a);
+  CHECK_CUDA(b);
+  TORCH_CHECK(w8 == 1 || w8 == 2, "gemm_w8: w8 must be 1 (A is the weight) or 2 (B)");
+  const at::Tensor& wt = w8 == 1 ? a : b;
+  const at::Tensor& act = w8 == 1 ? b : a;
+  TORCH_CHECK(wt.scalar_type() == at::kFloat8_e4m3fn, "gemm_w8: weight must be float8_e4m3fn");
+  CHECK_BF16(act);
+  TORCH_CHECK(scales.scalar_type() == at::kFloat && scales.dim() == 2 && scales.stride(1) == 1,
+              "gemm_w8: scales must be fp32 [row blocks, k blocks]");
+  const bool grouped = gtiles.has_value();
+  TORCH_CHECK(!grouped || w8 == 2, "gemm_w8: grouped mode takes the weight as B");
+  TORCH_CHECK(a.stride(-1) == 1 && b.stride(-1) == 1 && out.stride(-1) == 1,
+              "gemm_w8: inner dims must be contiguous");
+  const bool f32_out = (epi == b200::EPI_F32_RED || epi == b200::EPI_F32_RED_T);
+  TORCH_CHECK(out.scalar_type() == (f32_out ? at::kFloat : at::kBFloat16), "gemm_w8: out dtype");
+  const c10::cuda::CUDAGuard guard(a.device());
+  b200::GemmArgs g{};
+  g.A = a.data_ptr();
+  g.B = b.data_ptr();
+  g.out = out.data_ptr();
+  g.lda = a.stride(-2);
+  g.ldb = b.stride(-2);
+  g.ldo = out.stride(0);
+  g.M = (int)a.size(0);
+  g.K = (int)a.size(-1);
+  if (grouped) {
+    TORCH_CHECK(b.dim() == 3 && b.is_contiguous() && b.size(2) == a.size(1), "gemm_w8: grouped b");
+    TORCH_CHECK(b.size(1) % 128 == 0, "gemm_w8: grouped expert rows must be multiples of 128");
+    g.N = (int)b.size(1);
+    g.gtiles = gtiles->data_ptr<int>();
+    g.gcount = gcount.value().data_ptr<int>();
+    g.gmax = (int)gtiles->size(0);
+    g.num_groups = (int)b.size(0);
+  } else {
+    TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.size(1) == b.size(1), "gemm_w8: bad shapes");
+    g.N = (int)b.size(0);
+  }
+  g.bn = (int)bn;
+  g.epi = (int)epi;
+  g.splits = (int)splits;
+  g.status = status_word();
+  g.w8 = (int)w8;
+  g.w_scales = scales.data_ptr<float>();
+  g.w_scale_ld = (int)scales.stride(0);
+  g.w_scale_rows = (int)scales.size(0);
+  if (g.M == 0 || g.N == 0) return;
+  b200::gemm_bf16_launch(g, cur_stream());
+  check_launch("gemm_w8");
+}
+
 // FP8 (e4m3) GEMM with per-tensor scales: out = alpha * (a @ b^T) (epilogue as in `gemm`).
 void gemm_fp8(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, int64_t epi, int64_t bn,
               int64_t splits, double alpha) {
@@ -183,11 +240,19 @@ void rmsnorm_quant(const at::Tensor& x, const at::Tensor& w, double eps, at::Ten
 // owner; `out` is then only a shape / stride carrier).
 void gemm_sp(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, int64_t epi, int64_t bn,
              int64_t ag_ctr, const std::vector<int64_t>& ag_targets, int64_t ag_rows,
-             const std::vector<int64_t>& rs_out, const std::vector<int64_t>& rs_ctr, int64_t rs_rows) {
+             const std::vector<int64_t>& rs_out, const std::vector<int64_t>& rs_ctr, int64_t rs_rows,
+             c10::optional<at::Tensor> b_scales) {
   CHECK_CUDA(a);
   CHECK_CUDA(b);
   CHECK_BF16(a);
-  CHECK_BF16(b);
+  // b: bf16 weight, or a block-scaled FP8 weight with its fp32 128 x 128 block scales
+  if (b_scales.has_value()) {
+    TORCH_CHECK(b.scalar_type() == at::kFloat8_e4m3fn, "gemm_sp: block-FP8 weight must be e4m3");
+    TORCH_CHECK(b_scales->scalar_type() == at::kFloat && b_scales->dim() == 2 &&
+                    b_scales->stride(1) == 1, "gemm_sp: scales must be fp32 [row blocks, k blocks]");
+  } else {
+    CHECK_BF16(b);
+  }
   TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.size(1) == b.size(1), "gemm_sp: bad shapes");
   TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1 && out.stride(-1) == 1,
               "gemm_sp: inner dims must be contiguous");
@@ -220,6 +285,12 @@ void gemm_sp(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, int64_t 
   g.splits = 1;
   g.status = status_word();
   g.sp = &sp;
+  if (b_scales.has_value()) {
+    g.w8 = 2;
+    g.w_scales = b_scales->data_ptr<float>();
+    g.w_scale_ld = (int)b_scales->stride(0);
+    g.w_scale_rows = (int)b_scales->size(0);
+  }
   if (g.M == 0 || g.N == 0) return;
   b200::gemm_bf16_launch(g, cur_stream());
   check_launch("gemm_sp");
@@ -929,6 +1000,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_free", &symm_free);
   m.def("tensor_from_ptr", &tensor_from_ptr);
   m.def("tp_allreduce_norm", &tp_allreduce_norm);
+  m.def("gemm_w8", &gemm_w8);
   m.def("gemm_grouped", &gemm_grouped);
   m.def("moe_route", &moe_route);
   m.def("moe_align", &moe_align);

@@ -58,6 +58,13 @@ struct GemmArgs {
   // accumulator is multiplied by `alpha` (per-tensor scales a * b) in the epilogue.
   int fp8 = 0;
   float alpha = 1.f;
+  // Block-scaled FP8 weight (W8A16): w8 = 1 when A, 2 when B is the weight, held as e4m3 bytes
+  // with fp32 scales [w_scale_rows][w_scale_ld], one per 128 x 128 block (row block = weight
+  // row / 128, column = k / 128); the other operand is bf16.
+  int w8 = 0;
+  const float* w_scales = nullptr;
+  int w_scale_ld = 0;
+  int w_scale_rows = 0;
 };
 
 void gemm_bf16_launch(const GemmArgs& args, cudaStream_t stream);

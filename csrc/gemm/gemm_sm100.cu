@@ -71,6 +71,10 @@ struct GemmParams {
   const int* gcount;   // number of valid entries
   GemmSPArgs sp;       // sequence-parallel all-gather wait / reduce-scatter epilogue
   float alpha;         // epilogue scale of FP8 operands (1 for bf16)
+  // block-scaled FP8 weight operand (W8 kernels): fp32 scales [wsc_rows][wsc_ld], one per
+  // 128 x 128 block of the weight
+  const float* wsc;
+  int wsc_ld, wsc_rows;
 };
 
 // Bounded wait until a monotonic counter (written by a peer with a system-scope release)
@@ -186,12 +190,25 @@ __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)
 // FP8 = true: e4m3 operands (kind::f8f6f4).  A 128-byte swizzle row then holds 128 elements, so
 // the shared-memory tiles and the per-instruction descriptor advance (32 bytes) are unchanged;
 // only the k-block element count, the MMA kind and the epilogue scale differ.
-template <int BN, int STAGES, int EPI, bool FP8 = false>
-__global__ void __launch_bounds__(192, 1)
+//
+// W8 = 1 / 2: operand A / B is a block-scaled FP8 weight (e4m3 bytes, one fp32 scale per 128 x
+// 128 block) multiplied with bf16 activations.  TMA streams the weight tile as bytes (64 per
+// row, no swizzle) into a staging buffer; four converter warps (warps 6..9) widen it with the
+// tile's block scale, bf16(e4m3 * scale), into the 128-byte-swizzled bf16 operand layout the
+// MMA descriptors read, and release the stage to the MMA issuer (conv_bar).  Weight bytes cross
+// HBM once at one byte per element; the tensor cores run kind::f16.
+template <int BN, int STAGES, int EPI, bool FP8 = false, int W8 = 0>
+__global__ void __launch_bounds__(W8 ? 320 : 192, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA,
                      const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
   constexpr int kBTileBytes = BN * kBK * 2;
-  constexpr int kStageBytes = kATileBytes + kBTileBytes;
+  constexpr int kW8Rows = W8 == 1 ? kBM : W8 == 2 ? BN : 0;  // weight rows per tile
+  constexpr int kSBytes = kW8Rows * kBK;                      // fp8 staging bytes per stage
+  constexpr int kStageBytes = kATileBytes + kBTileBytes + kSBytes;
+  // bytes the TMA delivers per stage (the converted operand is written by the converter)
+  constexpr int kStageTx = W8 == 1   ? kSBytes + kBTileBytes
+                           : W8 == 2 ? kATileBytes + kSBytes
+                                     : kATileBytes + kBTileBytes;
   constexpr uint32_t kTmemCols = TmemCols<BN>::v;
   constexpr uint32_t kIdesc = make_idesc_f16(kBM, BN, !FP8);  // FP8: type fields 0 = E4M3
   constexpr int kKElems = FP8 ? 2 * kBK : kBK;                  // elements per k-block
@@ -202,9 +219,11 @@ __global__ void __launch_bounds__(192, 1)
                                              ~uintptr_t(1023));
   uint8_t* smA = smem;
   uint8_t* smB = smem + STAGES * kATileBytes;
+  uint8_t* smS = smB + STAGES * kBTileBytes;  // fp8 weight staging (W8)
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * kStageBytes);
   uint64_t* empty_bar = full_bar + STAGES;
-  uint64_t* tfull_bar = empty_bar + STAGES;
+  uint64_t* conv_bar = empty_bar + STAGES;  // converted operand ready (W8)
+  uint64_t* tfull_bar = conv_bar + STAGES;
   uint64_t* tempty_bar = tfull_bar + 2;
   uint32_t* tmem_base_smem = reinterpret_cast<uint32_t*>(tempty_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_smem + 1);
@@ -219,6 +238,7 @@ __global__ void __launch_bounds__(192, 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
+      mbar_init(&conv_bar[s], 4);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
@@ -261,11 +281,13 @@ __global__ void __launch_bounds__(192, 1)
           // peer stores (generic proxy) -> this thread's TMA reads (async proxy)
           if (waited) asm volatile("fence.proxy.async.global;" ::: "memory");
         }
-        tma_load_2d(&tmA, &full_bar[s], smA + s * kATileBytes, kb * kKElems, a_row, hint_a);
+        uint8_t* dst = W8 == 1 ? smS + s * kSBytes : smA + s * kATileBytes;
+        tma_load_2d(&tmA, &full_bar[s], dst, kb * kKElems, a_row, hint_a);
       };
       auto load_b = [&](int s, int kb, int nb, int mb) {
         const int base = p.grouped ? tile_rows(p, mb).b_base : 0;
-        tma_load_2d(&tmB, &full_bar[s], smB + s * kBTileBytes, kb * kKElems, base + nb * BN, hint_b);
+        uint8_t* dst = W8 == 2 ? smS + s * kSBytes : smB + s * kBTileBytes;
+        tma_load_2d(&tmB, &full_bar[s], dst, kb * kKElems, base + nb * BN, hint_b);
       };
       // The grouped tile list is written by the previous kernel.
       if (p.grouped) pdl_wait();
@@ -282,7 +304,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
       for (int i = 0; i < STAGES; ++i) {
         if (have) {
-          mbar_arrive_expect_tx(&full_bar[i], kStageBytes);
+          mbar_arrive_expect_tx(&full_bar[i], kStageTx);
           if (kWeightIsA) load_a(i, kb, mb); else load_b(i, kb, nb, mb);
           pre_mb[i] = mb;
           pre_nb[i] = nb;
@@ -310,7 +332,7 @@ __global__ void __launch_bounds__(192, 1)
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(&full_bar[s], kStageBytes);
+        mbar_arrive_expect_tx(&full_bar[s], kStageTx);
         load_a(s, kb, mb);
         load_b(s, kb, nb, mb);
         ++it;
@@ -349,7 +371,8 @@ __global__ void __launch_bounds__(192, 1)
         for (int kb = k0; kb < k1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
-          if (!mbar_wait_abortable(&full_bar[s], ph, kTimeoutTmaFull, p.status, abort_flag)) {
+          if (!mbar_wait_abortable(W8 ? &conv_bar[s] : &full_bar[s], ph, kTimeoutTmaFull, p.status,
+                                   abort_flag)) {
             ok = false;
             break;
           }
@@ -368,6 +391,59 @@ __global__ void __launch_bounds__(192, 1)
           umma_commit(&empty_bar[s]);
         }
         if (ok) umma_commit(&tfull_bar[acc]);
+      }
+    }
+  } else if (W8 != 0 && warp >= 6) {
+    // ------------------------------ fp8 -> bf16 weight converter ------------------------------
+    // Lane l of converter warp cw reads 16 staged bytes (row r, bytes 16 * (l % 4) ..) and
+    // writes them as 16 bf16 = 16-byte chunks 2 (l % 4) and 2 (l % 4) + 1 of the 128-byte
+    // operand row r, each at chunk ^ (r % 8) (the 128-byte swizzle on the 1024-byte-aligned
+    // tile).  Eight lanes of a phase cover two rows: conflict-free reads and writes.
+    if (p.grouped) pdl_wait();  // the tile list is written by the previous kernel
+    const int cw = warp - 6;
+    uint32_t it = 0;
+    bool ok = true;
+    SegCursor cur(p);
+    int mb, nb, k0, k1;
+    while (ok && cur.next(p, mb, nb, k0, k1)) {
+      const TileRows tr = tile_rows(p, mb);
+      const int wrow0 = W8 == 1 ? tr.a_row : tr.b_base + nb * BN;  // first weight row of the tile
+      for (int kb = k0; kb < k1; ++kb, ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        if (!mbar_wait_abortable(&full_bar[s], ph, kTimeoutTmaFull, p.status, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const uint8_t* src = smS + s * kSBytes;
+        uint8_t* dst = W8 == 1 ? smA + s * kATileBytes : smB + s * kBTileBytes;
+        const float* sc_col = p.wsc + (kb >> 1);  // 128-wide scale column of this 64-k block
+#pragma unroll
+        for (int i = 0; i < kW8Rows / 32; ++i) {
+          const int r = cw * (kW8Rows / 4) + i * 8 + (lane >> 2);
+          const int c16 = lane & 3;
+          const uint4 v = *reinterpret_cast<const uint4*>(src + r * kBK + c16 * 16);
+          const int srow = min((wrow0 + r) >> 7, p.wsc_rows - 1);
+          const float sc = __ldg(sc_col + (long long)srow * p.wsc_ld);
+          const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+          uint32_t o[8];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t lo = e4m3x2_to_f16x2(w4[j]), hi = e4m3x2_to_f16x2(w4[j] >> 16);
+            const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&lo));
+            const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&hi));
+            o[2 * j] = pack_bf16x2(a.x * sc, a.y * sc);
+            o[2 * j + 1] = pack_bf16x2(b.x * sc, b.y * sc);
+          }
+          uint8_t* drow = dst + r * 128;
+          const int sw = r & 7;
+          *reinterpret_cast<uint4*>(drow + (((2 * c16) ^ sw) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+          *reinterpret_cast<uint4*>(drow + (((2 * c16 + 1) ^ sw) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
+        }
+        // generic-proxy shared-memory writes -> the tensor cores' (async proxy) operand reads
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&conv_bar[s]);
       }
     }
   } else {
@@ -582,14 +658,16 @@ CUtensorMap make_tmap_u8_2d(const void* ptr, uint64_t inner, uint64_t outer, uin
   return m;
 }
 
-template <int BN, int STAGES, int EPI, bool FP8 = false>
+template <int BN, int STAGES, int EPI, bool FP8 = false, int W8 = 0>
 static void launch_impl(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
                         int grid, cudaStream_t stream) {
-  constexpr int smem = STAGES * (kATileBytes + BN * kBK * 2) + 1024 + 256;
-  auto kern = gemm_bf16_kernel<BN, STAGES, EPI, FP8>;
+  constexpr int w8_rows = W8 == 1 ? kBM : W8 == 2 ? BN : 0;
+  constexpr int smem = STAGES * (kATileBytes + BN * kBK * 2 + w8_rows * kBK) + 1024 + 256;
+  static_assert(smem <= 232448, "shared memory budget");
+  auto kern = gemm_bf16_kernel<BN, STAGES, EPI, FP8, W8>;
   static std::atomic<uint64_t> configured{0};  // per instantiation, per device
   set_max_dynamic_smem_once(kern, smem, configured);
-  launch_pdl(kern, dim3(grid), dim3(192), smem, stream, ta, tb, p);
+  launch_pdl(kern, dim3(grid), dim3(W8 ? 320 : 192), smem, stream, ta, tb, p);
 }
 
 int num_sms_cached() {
@@ -615,10 +693,23 @@ void gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
   if (a.fp8 && (grouped || a.sp != nullptr))
     throw std::invalid_argument("gemm: FP8 operands are for the dense (non-grouped, non-SP) modes");
   const uint64_t b_rows = grouped ? (uint64_t)a.N * a.num_groups : (uint64_t)a.N;
-  const CUtensorMap ta = a.fp8 ? make_tmap_u8_2d(a.A, a.K, a.M, a.lda, 128, kBM, 128)
-                               : make_tmap_bf16_2d(a.A, a.K, a.M, a.lda, kBK, kBM, true);
-  const CUtensorMap tb = a.fp8 ? make_tmap_u8_2d(a.B, a.K, b_rows, a.ldb, 128, bn, 128)
-                               : make_tmap_bf16_2d(a.B, a.K, b_rows, a.ldb, kBK, bn, true);
+  if (a.w8 != 0) {
+    if (a.fp8 || (a.w8 != 1 && a.w8 != 2) || a.w_scales == nullptr || a.w_scale_rows < 1 ||
+        a.w_scale_ld < (a.K + 127) / 128)
+      throw std::invalid_argument("gemm: bad block-FP8 weight arguments");
+    if (a.K % 16 != 0 || (a.w8 == 1 ? a.lda : a.ldb) % 16 != 0)
+      throw std::invalid_argument("gemm: block-FP8 weight rows must be multiples of 16 bytes");
+    const uint64_t wrows = a.w8 == 1 ? (uint64_t)a.M : b_rows;
+    if ((uint64_t)a.w_scale_rows < (wrows + 127) / 128)
+      throw std::invalid_argument("gemm: block-FP8 scale rows do not cover the weight rows");
+  }
+  // block-FP8 weight operand: bytes, 64 per row per stage, no swizzle (the converter swizzles)
+  const CUtensorMap ta = a.w8 == 1 ? make_tmap_u8_2d(a.A, a.K, a.M, a.lda, kBK, kBM, 0)
+                         : a.fp8   ? make_tmap_u8_2d(a.A, a.K, a.M, a.lda, 128, kBM, 128)
+                                   : make_tmap_bf16_2d(a.A, a.K, a.M, a.lda, kBK, kBM, true);
+  const CUtensorMap tb = a.w8 == 2 ? make_tmap_u8_2d(a.B, a.K, b_rows, a.ldb, kBK, bn, 0)
+                         : a.fp8   ? make_tmap_u8_2d(a.B, a.K, b_rows, a.ldb, 128, bn, 128)
+                                   : make_tmap_bf16_2d(a.B, a.K, b_rows, a.ldb, kBK, bn, true);
   GemmParams p;
   p.grouped = grouped ? 1 : 0;
   p.gtiles = reinterpret_cast<const int4*>(a.gtiles);
@@ -631,6 +722,9 @@ void gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
   if (a.epi == EPI_SILU_BF16) p.num_n_blocks = (a.N + bn - 1) / bn;  // N = 2 * I (interleaved)
   p.num_k_blocks = (a.K + kelems - 1) / kelems;
   p.alpha = a.fp8 ? a.alpha : 1.f;
+  p.wsc = a.w_scales;
+  p.wsc_ld = a.w_scale_ld;
+  p.wsc_rows = a.w_scale_rows;
   p.streamk = a.splits < 0 ? 1 : 0;
   int splits = a.splits < 1 ? 1 : a.splits;
   if (splits > p.num_k_blocks) splits = p.num_k_blocks;
@@ -682,6 +776,33 @@ void gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
                                 std::to_string(bn) + " epi=" + std::to_string(a.epi));
   }
 #undef B200_GEMM_FP8_CASE
+#define B200_GEMM_W8_CASE(W8_, BN_, ST_, EPI_)                           \
+  if (a.w8 == W8_ && bn == BN_ && a.epi == EPI_) {                        \
+    launch_impl<BN_, ST_, EPI_, false, W8_>(ta, tb, p, grid, stream);     \
+    return;                                                               \
+  }
+  if (a.w8 != 0) {
+    // weights as A: decode (swapped operands) -- split-K fp32 reductions
+    B200_GEMM_W8_CASE(1, 16, 8, EPI_F32_RED_T)
+    B200_GEMM_W8_CASE(1, 32, 8, EPI_F32_RED_T)
+    B200_GEMM_W8_CASE(1, 64, 7, EPI_F32_RED_T)
+    B200_GEMM_W8_CASE(1, 128, 5, EPI_F32_RED_T)
+    B200_GEMM_W8_CASE(1, 16, 8, EPI_BF16_T)
+    B200_GEMM_W8_CASE(1, 32, 8, EPI_BF16_T)
+    B200_GEMM_W8_CASE(1, 64, 7, EPI_BF16_T)
+    B200_GEMM_W8_CASE(1, 128, 5, EPI_BF16_T)
+    // weights as B: prefill / grouped experts
+    B200_GEMM_W8_CASE(2, 256, 3, EPI_BF16)
+    B200_GEMM_W8_CASE(2, 128, 5, EPI_BF16)
+    B200_GEMM_W8_CASE(2, 256, 3, EPI_SILU_BF16)
+    B200_GEMM_W8_CASE(2, 128, 5, EPI_F32_RED)
+    B200_GEMM_W8_CASE(2, 256, 3, EPI_BF16_RS)
+    B200_GEMM_W8_CASE(2, 128, 5, EPI_BF16_RS)
+    throw std::invalid_argument("gemm (block fp8): unsupported (operand, bn, epilogue): w8=" +
+                                std::to_string(a.w8) + " bn=" + std::to_string(bn) +
+                                " epi=" + std::to_string(a.epi));
+  }
+#undef B200_GEMM_W8_CASE
 #define B200_GEMM_CASE(BN_, ST_, EPI_)                                    \
   if (bn == BN_ && a.epi == EPI_) {                                       \
     launch_impl<BN_, ST_, EPI_>(ta, tb, p, grid, stream);                 \

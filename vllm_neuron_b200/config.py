@@ -238,5 +238,6 @@ class B200Config:
                 setattr(self, name, sorted(set(v)))
         if self.all2all_backend not in (None, "neuron", "nvlink", "nccl"):
             raise ValueError(f"unknown all2all_backend {self.all2all_backend!r}")
-        if self.quantization not in (None, "fp8", "fp8_static", "mxfp4", "mxfp8", "modelopt_fp8"):
+        if self.quantization not in (None, "fp8", "fp8_static", "fp8_block", "mxfp4", "mxfp8",
+                                     "modelopt_fp8", "bf16", "none"):
             raise ValueError(f"unknown quantization {self.quantization!r}")

@@ -113,6 +113,14 @@ def build_model(args: EngineArgs, tp: GroupComm = SINGLE):
         if not hasattr(model, "quantize_fp8_static"):
             raise ValueError(f"{type(model).__name__} does not support static FP8 linears")
         model.quantize_fp8_static(fp8_scales)
+    elif b200_config.quantization == "fp8_block" or (
+            model_path is not None and getattr(arch, "weight_block_size", None)
+            and b200_config.quantization not in ("bf16", "none")):
+        # block-scaled FP8 (128 x 128): checkpoints with weight_scale_inv, or random-init
+        # weights quantized with quantization="fp8_block"
+        if not hasattr(model, "quantize_block_fp8"):
+            raise ValueError(f"{type(model).__name__} does not support block-FP8 linears")
+        model.quantize_block_fp8()
     if args.kv_cache_dtype not in (None, "auto"):
         if not hasattr(model, "set_kv_cache_dtype"):
             raise ValueError(f"{type(model).__name__} does not support kv_cache_dtype={args.kv_cache_dtype!r}")

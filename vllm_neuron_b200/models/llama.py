@@ -206,7 +206,7 @@ class LlamaForCausalLM(torch.nn.Module):
             # and the norm: dense SwiGLU decoders without an o_proj bias
             if (self.sequence_parallel and type(self)._mlp is LlamaForCausalLM._mlp
                     and all(getattr(ly, "o_bias", None) is None for ly in self.layers)
-                    and not getattr(self, "fp8_linears", 0)):
+                    and (not getattr(self, "fp8_linears", 0) or getattr(self, "block_fp8", False))):
                 from ..parallel.fused import SPFusedComm
 
                 self.sp_fused = SPFusedComm(self.tp, self.H, self.max_tokens + self.tp.world, self.device,
@@ -239,6 +239,11 @@ class LlamaForCausalLM(torch.nn.Module):
         sc = getattr(self, "kv_scales", None)
         return sc[kv_layer] if sc else (1.0, 1.0)
 
+    # weights that block-FP8 serving quantizes (2-D linears, 3-D expert stacks); the router,
+    # norms, embeddings and LM head stay bf16
+    BLOCK_FP8_PARAMS = ("qkv", "o", "gate_up", "down", "w_gu", "w_down", "sh_gu", "sh_down",
+                        "w_in", "out_proj", "qkvg")
+
     # projections of a decoder layer and the checkpoint names whose scales they take
     FP8_LINEARS = (("qkv", ("q_proj", "k_proj", "v_proj")), ("o", ("o_proj",)),
                    ("gate_up", ("gate_proj", "up_proj")), ("down", ("down_proj",)))
@@ -268,6 +273,32 @@ class LlamaForCausalLM(torch.nn.Module):
                 setattr(ly, name, fw)
                 n += 1
         self.fp8_linears = n
+        return n
+
+    @torch.no_grad()
+    def quantize_block_fp8(self) -> int:
+        """Switch the dense projections to block-scaled FP8 weights (e4m3, one fp32 scale per
+        128 x 128 block of the rank's fused shard; W8A16 on the tcgen05 GEMM).  A block-FP8
+        checkpoint whose blocks align with the shard (rows and K in multiples of 128, as for
+        Llama-3-70B at TP 8) is recovered exactly: its values re-quantize to the same bytes.
+        Random-init weights are quantized from their bf16 draw (``quantization: fp8_block``)."""
+        n = 0
+        for ly in self.layers:
+            for name in self.BLOCK_FP8_PARAMS:
+                w = getattr(ly, name, None)
+                if w is None or not isinstance(w, torch.Tensor) or w.dim() not in (2, 3):
+                    continue
+                if w.dim() == 3 and w.shape[1] % L.BlockFP8Weight.BLOCK:
+                    continue  # stacked experts need 128-row experts
+                bw = L.BlockFP8Weight.from_weight(w)
+                if name in getattr(ly, "_parameters", {}):
+                    del ly._parameters[name]
+                setattr(ly, name, bw)
+                n += 1
+        self.fp8_linears = n
+        self.block_fp8 = True
+        if self.device.type == "cuda":
+            torch.cuda.empty_cache()
         return n
 
     def set_kv_cache_dtype(self, kv_cache_dtype: str, scales: list[tuple[float, float]] | None = None):

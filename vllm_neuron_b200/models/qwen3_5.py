@@ -95,6 +95,7 @@ class Qwen3_5MoeForCausalLM(Qwen3MoeForCausalLM):
     def num_kv_layers(self) -> int:
         return len(self.attn_layers)
 
+
     @torch.no_grad()
     def init_random(self, seed: int = 0, std: float = 0.02):
         super().init_random(seed, std)

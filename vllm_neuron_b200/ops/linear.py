@@ -64,6 +64,61 @@ class FP8Weight:
         return self.q.float() * self.w_scale
 
 
+class BlockFP8Weight:
+    """Block-scaled FP8 weight ``[N, K]`` (or stacked experts ``[E, N, K]``): e4m3 values ``q``
+    and one fp32 scale per 128 x 128 block, ``scales [ceil(rows / 128), ceil(K / 128)]`` over the
+    (stacked) rows, true weight = ``q * scale`` -- the layout of DeepSeek / Qwen FP8 checkpoints
+    (``weight`` + ``weight_scale_inv``).  Served W8A16: the GEMM streams the fp8 bytes and widens
+    each weight tile in shared memory with its block scale (bf16 activations, fp32 accumulation),
+    so decode reads half the bytes of bf16 weights.  Expert stacks need rows per expert to be a
+    multiple of 128."""
+
+    BLOCK = 128
+
+    def __init__(self, q: torch.Tensor, scales: torch.Tensor):
+        assert q.dtype == torch.float8_e4m3fn and q.dim() in (2, 3)
+        rows = q.shape[0] * q.shape[1] if q.dim() == 3 else q.shape[0]
+        assert scales.dtype == torch.float32 and scales.dim() == 2
+        assert scales.shape[0] == -(-rows // self.BLOCK) and scales.shape[1] == -(-q.shape[-1] // self.BLOCK)
+        self.q = q
+        self.scales = scales
+
+    @classmethod
+    def from_weight(cls, w: torch.Tensor) -> "BlockFP8Weight":
+        """Quantize ``w`` per 128 x 128 block with scale ``amax / 448``."""
+        w = w.detach()
+        shp = w.shape
+        w2 = w.reshape(-1, shp[-1])
+        N, K = w2.shape
+        B = cls.BLOCK
+        nb, kb = -(-N // B), -(-K // B)
+        pad = torch.zeros(nb * B, kb * B, dtype=torch.float32, device=w.device)
+        pad[:N, :K] = w2.float()
+        blk = pad.view(nb, B, kb, B)
+        sc = (blk.abs().amax(dim=(1, 3)) / FP8_MAX).clamp_min(1e-12)
+        q = (blk / sc[:, None, :, None]).clamp(-FP8_MAX, FP8_MAX).view(nb * B, kb * B)[:N, :K]
+        return cls(q.to(torch.float8_e4m3fn).reshape(shp).contiguous(), sc.contiguous())
+
+    @property
+    def shape(self):
+        return self.q.shape
+
+    @property
+    def device(self):
+        return self.q.device
+
+    def dequant(self, dtype=torch.float32) -> torch.Tensor:
+        """``q * scale`` (the fp32 oracle; the kernels round each product to bf16)."""
+        q2 = self.q.reshape(-1, self.q.shape[-1]).float()
+        B = self.BLOCK
+        s = self.scales.repeat_interleave(B, 0)[: q2.shape[0]].repeat_interleave(B, 1)[:, : q2.shape[1]]
+        return (q2 * s).to(dtype).reshape(self.q.shape)
+
+    def dequant_bf16_ref(self) -> torch.Tensor:
+        """``bf16(q * scale)``: exactly the operand the tensor cores multiply."""
+        return self.dequant(torch.float32).to(torch.bfloat16)
+
+
 def quantize_fp8(x: torch.Tensor, scale: float, out: torch.Tensor | None = None) -> torch.Tensor:
     """``satfinite(x / scale)`` as ``torch.float8_e4m3fn`` (the rule of the quant kernels)."""
     if out is None:
@@ -178,6 +233,13 @@ def gemm_out(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,
         ext().gemm_fp8(xq, w.q, out, EPI_BF16, bn or _pick_bn_wide(M, N, num_sms(x.device)), 1,
                        w.in_scale * w.w_scale)
         return out
+    if isinstance(w, BlockFP8Weight):
+        if not x.is_cuda:
+            out.copy_((x.float() @ w.dequant_bf16_ref().float().t()).to(out.dtype))
+            return out
+        ext().gemm_w8(x, w.q, out, EPI_BF16, bn or _pick_bn_wide(M, N, num_sms(x.device)), 1,
+                      w.scales, 2, None, None)
+        return out
     if not x.is_cuda:
         out.copy_((x.float() @ w.float().t()).to(out.dtype))
         return out
@@ -194,8 +256,15 @@ def gemm_skinny_bf16(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None 
     """Decode regime without split-K: swapped operands, transposed bf16 store."""
     M, K = x.shape
     N = w.shape[0]
-    if isinstance(w, FP8Weight):  # FP8 keeps the row-major regime (no transposed FP8 store)
+    if isinstance(w, FP8Weight):  # row-major regime (no transposed FP8 store)
         return gemm_out(x, w, out)
+    if isinstance(w, BlockFP8Weight):
+        if out is None:
+            out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+        if not x.is_cuda:
+            return gemm_out(x, w, out)
+        ext().gemm_w8(w.q, x, out, EPI_BF16_T, skinny_bn(M), 1, w.scales, 1, None, None)
+        return out
     if out is None:
         out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
     if not x.is_cuda:
@@ -230,6 +299,19 @@ def gemm_accumulate(x: torch.Tensor, w: torch.Tensor, acc: torch.Tensor,
             rows = math.ceil(M / 128) * 128 * math.ceil(N / 128)
             s = splits if splits is not None else pick_splits(rows, K, sms, 128)
             ext().gemm_fp8(xq, w.q, acc, EPI_F32_RED, 128, s, w.in_scale * w.w_scale)
+        return acc
+    if isinstance(w, BlockFP8Weight):
+        if not x.is_cuda:
+            acc[:M].add_(x.float() @ w.dequant_bf16_ref().float().t())
+            return acc
+        sms = num_sms(x.device)
+        if M <= SKINNY_MAX:
+            s = splits if splits is not None else pick_splits(N, K, sms)
+            ext().gemm_w8(w.q, x, acc, EPI_F32_RED_T, skinny_bn(M), s, w.scales, 1, None, None)
+        else:
+            rows = math.ceil(M / 128) * 128 * math.ceil(N / 128)
+            s = splits if splits is not None else pick_splits(rows, K, sms)
+            ext().gemm_w8(x, w.q, acc, EPI_F32_RED, 128, s, w.scales, 2, None, None)
         return acc
     if not x.is_cuda:
         acc[:M].add_(x.float() @ w.float().t())
@@ -267,6 +349,13 @@ def gemm_silu(x: torch.Tensor, w_gu: torch.Tensor, out: torch.Tensor | None = No
             out.copy_(silu_mul_ref(_fp8_ref(xq, w_gu), SILU_BLOCK).to(out.dtype))
             return out
         ext().gemm_fp8(xq, w_gu.q, out, EPI_SILU_BF16, 2 * SILU_BLOCK, 1, w_gu.in_scale * w_gu.w_scale)
+        return out
+    if isinstance(w_gu, BlockFP8Weight):
+        if not x.is_cuda:
+            y = x.float() @ w_gu.dequant_bf16_ref().float().t()
+            out.copy_(silu_mul_ref(y, SILU_BLOCK).to(out.dtype))
+            return out
+        ext().gemm_w8(x, w_gu.q, out, EPI_SILU_BF16, 2 * SILU_BLOCK, 1, w_gu.scales, 2, None, None)
         return out
     if not x.is_cuda:
         y = x.float() @ w_gu.float().t()

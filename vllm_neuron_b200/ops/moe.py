@@ -115,11 +115,17 @@ def route_ref(logits: torch.Tensor, k: int, mode: int, renorm: bool = True,
     return i.to(torch.int32), v * scale
 
 
+def _dense(w):
+    """bf16 tensor view of a weight (block-FP8 weights: the bf16 operand the kernels use)."""
+    return w.dequant_bf16_ref() if isinstance(w, L.BlockFP8Weight) else w
+
+
 def experts_ref(x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, w_gu: torch.Tensor,
                 w_down: torch.Tensor, b_gu: torch.Tensor | None = None,
                 b_down: torch.Tensor | None = None, act: int = ACT_SILU, alpha: float = 1.702,
                 limit: float = 7.0, e_start: int = 0) -> torch.Tensor:
     """fp32 per-token loop: sum_j w_j * expert_{ids_j}(x) over the local experts."""
+    w_gu, w_down = _dense(w_gu), _dense(w_down)
     T, H = x.shape
     e_local, I2, _ = w_gu.shape
     I = I2 // 2
@@ -205,6 +211,7 @@ def mxfp4_gemm_ref(x: torch.Tensor, rows_expert: torch.Tensor, w_bf16: torch.Ten
 
 
 def shared_expert_ref(x: torch.Tensor, w_gu: torch.Tensor, w_down: torch.Tensor) -> torch.Tensor:
+    w_gu, w_down = _dense(w_gu), _dense(w_down)
     I = w_gu.shape[0] // 2
     h = x.float() @ w_gu.float().t()
     return (torch.nn.functional.silu(h[:, :I]) * h[:, I:]) @ w_down.float().t()
@@ -314,14 +321,19 @@ def _experts_cuda(x, ids, w, w_gu, w_down, k, b_gu, b_down, act, alpha, limit, e
     gt = ws.gtiles[:min(ws.gtiles.shape[0], R)]
     if use_fp4:
         ext().moe_mxfp4_gemm(xp, fp4_gu, gu, gt, ws.gcount)
+    elif isinstance(w_gu, L.BlockFP8Weight):
+        ext().gemm_w8(xp, w_gu.q, gu, EPI_BF16, 256, 1, w_gu.scales, 2, ws.gtiles, ws.gcount)
     else:
         ext().gemm_grouped(xp, w_gu, gu, ws.gtiles, ws.gcount, EPI_BF16, 256)
     a = ws.act[:R, :I]
     ext().moe_act(gu, b_gu, ws.row_expert, ws.offsets, act, alpha, limit, a)
     y = ws.y[:R]
+    bn_down = 256 if H % 256 == 0 else 128
     if use_fp4:
         ext().moe_mxfp4_gemm(a, fp4_down, y, gt, ws.gcount)
+    elif isinstance(w_down, L.BlockFP8Weight):
+        ext().gemm_w8(a, w_down.q, y, EPI_BF16, bn_down, 1, w_down.scales, 2, ws.gtiles, ws.gcount)
     else:
-        ext().gemm_grouped(a, w_down, y, ws.gtiles, ws.gcount, EPI_BF16, 256 if H % 256 == 0 else 128)
+        ext().gemm_grouped(a, w_down, y, ws.gtiles, ws.gcount, EPI_BF16, bn_down)
     ext().moe_combine(y, ws.inv_pos[:R], w, ids, b_down, e_start, shared, shared_gate, out)
     return out

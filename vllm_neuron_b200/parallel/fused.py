@@ -180,9 +180,17 @@ class SPFusedComm:
         self._Tl = Tl
         return self.x_view(par, Tl * self.W)
 
-    def gemm_ag(self, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, epi: int, bn: int) -> torch.Tensor:
+    @staticmethod
+    def _w(w):
+        """(weight tensor, block scales or None): bf16 weights or block-scaled FP8 ones."""
+        from ..ops.linear import BlockFP8Weight
+
+        return (w.q, w.scales) if isinstance(w, BlockFP8Weight) else (w, None)
+
+    def gemm_ag(self, x: torch.Tensor, w, out: torch.Tensor, epi: int, bn: int) -> torch.Tensor:
         """GEMM over the all-gathered rows ``x`` (a view from :meth:`norm_push`)."""
-        ext().gemm_sp(x, w, out, epi, bn, self._ag_ctr(self.rank, 0), self.ag_target, self._Tl, [], [], 0)
+        wt, sc = self._w(w)
+        ext().gemm_sp(x, wt, out, epi, bn, self._ag_ctr(self.rank, 0), self.ag_target, self._Tl, [], [], 0, sc)
         return out
 
     def gemm_rs(self, a: torch.Tensor, w: torch.Tensor, bn: int) -> None:
@@ -192,9 +200,10 @@ class SPFusedComm:
         par = self.rs_calls % 2
         self.rs_calls += 1
         carrier = self.x_view(0, 1)  # row stride H for the slot stores
-        ext().gemm_sp(a, w, carrier, 5, bn, 0, [], 0,
+        wt, sc = self._w(w)
+        ext().gemm_sp(a, wt, carrier, 5, bn, 0, [], 0,
                       [self._slot(r, par, self.rank) for r in range(self.W)],
-                      [self._rs_ctr(r, self.rank) for r in range(self.W)], Tl)
+                      [self._rs_ctr(r, self.rank) for r in range(self.W)], Tl, sc)
         nb = -(-N // bn)
         lo, hi = (self.rank * Tl) // 128, ((self.rank + 1) * Tl - 1) // 128
         self.rs_target += (hi - lo + 1) * nb
