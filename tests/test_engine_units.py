@@ -18,12 +18,16 @@ def test_b200_config_accepts_reference_keys():
     assert c.num_batched_tokens_buckets == [128, 256, 512]
     assert c.on_device_sampling_config.global_topk == 64 and c.on_device_sampling_config.enabled
     assert c.extra == {"unknown_key": 1}
-    assert B200Config.from_additional_config({"b200_config": {"mlp_dp_size": 2}}).mlp_dp_size == 2
     with pytest.raises(ValueError):
         B200Config.from_dict({"attention_dp_size": 0})
     with pytest.raises(ValueError):
         B200Config.from_dict({"quantization": "int3"})
-    assert not B200Config.from_dict({"on_device_sampling_config": None}).on_device_sampling_config.enabled
+    # options of the reference that are not implemented are refused, not silently ignored
+    for bad in ({"mlp_dp_size": 2}, {"embedding_dp_size": 2}, {"lm_head_dp_size": 4},
+                {"fp8_packed_kv": True}, {"kv_segment_size_buckets": [512]},
+                {"decode_context_length_buckets": [1024]}, {"on_device_sampling_config": None}):
+        with pytest.raises(NotImplementedError):
+            B200Config.from_dict(bad)
 
 
 def test_arch_config_rope_formats():

@@ -241,3 +241,29 @@ class B200Config:
         if self.quantization not in (None, "fp8", "fp8_static", "fp8_block", "mxfp4", "mxfp8",
                                      "modelopt_fp8", "bf16", "none"):
             raise ValueError(f"unknown quantization {self.quantization!r}")
+        # Options of the reference this framework does not implement are refused rather than
+        # silently ignored, so a migrated configuration never changes meaning quietly.
+        for name in ("embedding_dp_size", "lm_head_dp_size", "mlp_dp_size"):
+            if getattr(self, name) > 1:
+                raise NotImplementedError(
+                    f"{name}={getattr(self, name)}: component data parallelism is not implemented; "
+                    "the embedding, MLP and LM head run tensor parallel over the whole TP group")
+        if self.fp8_packed_kv:
+            raise NotImplementedError("fp8_packed_kv: the packed FP8 K layout is not implemented; "
+                                      "use kv_cache_dtype='fp8' (e4m3 K/V, unpacked)")
+        if self.kv_segment_size_buckets is not None:
+            raise NotImplementedError(
+                "kv_segment_size_buckets: KV segments are not bucketed here (the decode kernel "
+                "splits each sequence's KV on the device by its real length); remove the option")
+        if self.decode_context_length_buckets is not None:
+            raise NotImplementedError(
+                "decode_context_length_buckets: decode graphs are captured per batch-size bucket "
+                "and the split-KV factor follows each step's real context lengths on the device; "
+                "remove the option")
+        if not self.on_device_sampling_config.enabled:
+            raise NotImplementedError("on_device_sampling_config=None: sampling always runs on the "
+                                      "device here (logits never leave the GPU)")
+        if self.max_logprobs < 0:
+            raise ValueError("max_logprobs must be >= 0")
+        if self.modules_to_not_convert is not None and not all(isinstance(m, str) for m in self.modules_to_not_convert):
+            raise ValueError("modules_to_not_convert must be a list of module names")

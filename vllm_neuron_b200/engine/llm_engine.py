@@ -115,9 +115,11 @@ def build_model(args: EngineArgs, tp: GroupComm = SINGLE):
         model.quantize_fp8_static(fp8_scales)
     elif b200_config.quantization == "fp8_block" or (
             model_path is not None and getattr(arch, "weight_block_size", None)
+            and device.type == "cuda" and dtype == torch.bfloat16
             and b200_config.quantization not in ("bf16", "none")):
-        # block-scaled FP8 (128 x 128): checkpoints with weight_scale_inv, or random-init
-        # weights quantized with quantization="fp8_block"
+        # block-scaled FP8 (128 x 128): checkpoints with weight_scale_inv served on the GPU, or
+        # random-init weights quantized with quantization="fp8_block" (CPU fp32 runs of a
+        # block-FP8 checkpoint keep the exact dequantized weights as the oracle)
         if not hasattr(model, "quantize_block_fp8"):
             raise ValueError(f"{type(model).__name__} does not support block-FP8 linears")
         model.quantize_block_fp8()
@@ -126,6 +128,11 @@ def build_model(args: EngineArgs, tp: GroupComm = SINGLE):
             raise ValueError(f"{type(model).__name__} does not support kv_cache_dtype={args.kv_cache_dtype!r}")
         model.set_kv_cache_dtype(args.kv_cache_dtype, _kv_scales_from_checkpoint(model, model_path))
     real_group = tp.world > 1 and tp.group is not None
+    if b200_config.attention_dp_size > 1:
+        raise NotImplementedError(
+            f"attention_dp_size={b200_config.attention_dp_size}: attention data parallelism is not "
+            "implemented; attention runs tensor parallel over the TP group (KV heads replicated "
+            "when TP exceeds their count), or use decode_context_parallel_size to shard KV tokens")
     # same-box comparison build: dense projections on cuBLAS (and, with fused_comm off, NCCL)
     from ..ops import linear as _lin
 
@@ -310,6 +317,7 @@ class LLMEngine:
         of the P prompt positions (reference: merge_prompt_embeds,
         vllm_neuron/functional/prompt_embeds.py:7); ``prompt_token_ids`` then only gives P."""
         params = SamplingParams.coerce(params)
+        self.validate_request(params)
         rid = request_id if request_id is not None else str(next(self._ids))
         req = Request(rid, list(prompt_token_ids), params, eos_token_id=self.eos_token_id,
                       prompt_embeds=prompt_embeds, mm=mm)
@@ -327,6 +335,21 @@ class LLMEngine:
             self._free_slots.append(req.slot)
             raise
         return rid
+
+    def validate_request(self, params: SamplingParams):
+        """Refuse what this engine was configured not to serve (reference: the platform's
+        request validation, vllm_neuron/vllm/platform.py:446-485): structured outputs when
+        ``enable_structured_outputs`` is off, and more logprobs than ``max_logprobs`` (0 = no
+        cap; only the sampled token's logprob is returned)."""
+        cfg = self.b200_config
+        if params.structured_outputs and not cfg.enable_structured_outputs:
+            raise ValueError("structured outputs are disabled (enable_structured_outputs=False)")
+        if params.logprobs and cfg.max_logprobs and params.logprobs > cfg.max_logprobs:
+            raise ValueError(f"logprobs={params.logprobs} exceeds max_logprobs={cfg.max_logprobs}")
+        if params.top_k and cfg.on_device_sampling_config.global_topk and \
+                params.top_k > cfg.on_device_sampling_config.global_topk:
+            raise ValueError(f"top_k={params.top_k} exceeds the on-device sampler's global_topk="
+                             f"{cfg.on_device_sampling_config.global_topk}")
 
     def abort_request(self, request_id: str):
         req = self.scheduler.requests.get(request_id)
