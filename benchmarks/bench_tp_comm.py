@@ -2,8 +2,8 @@
 
     torchrun --nproc-per-node N --master-addr 127.0.0.1 benchmarks/bench_tp_comm.py [--hidden 4096]
 
-For each row count T it checks, on the first call, that the fused kernel (grid form and the
-one-CTA-per-row form) gives the same residual and normalized rows as NCCL all-reduce +
+For each row count T it checks, on the first call, that the fused kernel (sentinel-polled
+form and the per-row-flag form) gives the same residual and normalized rows as NCCL all-reduce +
 add_rmsnorm (and that every rank holds identical rows), then times each path as a CUDA graph
 of ``--calls`` back-to-back calls (CUDA events, after warm-up replays; max over ranks).
 
@@ -50,8 +50,9 @@ def main():
     H = args.hidden
     rows = [int(r) for r in args.rows.split(",")]
     Tmax = max(rows)
-    fused = TPFusedComm(tp, H, Tmax, dev, cpu)
-    w = (1.0 + 0.1 * torch.randn(H, device=dev)).to(torch.bfloat16)
+    comms = [TPFusedComm(tp, H, Tmax, dev, cpu, algo=a) for a in (0, 1)]  # one object per form
+    w = (1.0 + 0.1 * torch.randn(H, device=dev, generator=torch.Generator(device=dev).manual_seed(3))
+         ).to(torch.bfloat16)
     eps = 1e-5
     g = torch.Generator(device=dev).manual_seed(100 + rank)
     acc = torch.zeros(Tmax, H, dtype=torch.float32, device=dev)
@@ -100,7 +101,7 @@ def main():
         ref_out = (xf * torch.rsqrt((xf * xf).mean(-1, keepdim=True) + eps) * w.float()).to(torch.bfloat16)
         row = {"T": T, "H": H, "world": world}
         for algo in (0, 1):
-            fused.algo = algo
+            fused = comms[algo]
             acc[:T].copy_(part)
             res[:T].copy_(res0[:T])
             fused.allreduce_norm(acc[:T], res[:T], w, eps, out[:T])
@@ -117,7 +118,6 @@ def main():
             row[f"algo{algo}_max_err_out"] = d_out
             row[f"algo{algo}_ranks_identical"] = same
             row[f"algo{algo}_us"] = timed(lambda: fused.allreduce_norm(acc[:T], res[:T], w, eps, out[:T]))
-        fused.algo = 0
 
         def nccl():
             tp.all_reduce_(acc[:T])
@@ -132,7 +132,8 @@ def main():
         if rank == 0:
             print(json.dumps(row), flush=True)
     assert ext().read_status() == 0
-    fused.close()
+    for c in comms:
+        c.close()
     dist.barrier()
     if rank == 0:
         print("done", flush=True)

@@ -617,9 +617,9 @@ static void fill_ptrs(const std::vector<int64_t>& v, void** dst, const char* wha
 // residual += all_reduce(acc) over the TP group (one-shot push through symmetric peer
 // memory), out = rmsnorm(residual) * w; acc is cleared.
 void tp_allreduce_norm(at::Tensor& acc, const std::vector<int64_t>& recv_ptrs,
-                       const std::vector<int64_t>& flag_ptrs, const std::vector<int64_t>& ctr_ptrs,
-                       at::Tensor& state, at::Tensor& residual, const at::Tensor& w, at::Tensor& out,
-                       double eps, int64_t rank, int64_t max_rows, int64_t algo) {
+                       const std::vector<int64_t>& flag_ptrs, at::Tensor& state, at::Tensor& residual,
+                       const at::Tensor& w, at::Tensor& out, double eps, int64_t rank,
+                       int64_t max_rows, int64_t algo) {
   CHECK_CUDA(acc);
   TORCH_CHECK(acc.scalar_type() == at::kFloat, "acc must be fp32");
   CHECK_BF16(residual);
@@ -634,8 +634,6 @@ void tp_allreduce_norm(at::Tensor& acc, const std::vector<int64_t>& recv_ptrs,
   p.acc_stride = acc.stride(0);
   fill_ptrs(recv_ptrs, (void**)p.recv_peers, "recv");
   fill_ptrs(flag_ptrs, (void**)p.flag_peers, "flags");
-  TORCH_CHECK(ctr_ptrs.size() == recv_ptrs.size(), "recv/counter pointer lists differ");
-  fill_ptrs(ctr_ptrs, (void**)p.ctr_peers, "counters");
   TORCH_CHECK(state.scalar_type() == at::kLong && state.numel() >= 4, "state must be int64[4]");
   p.state = (unsigned long long*)state.data_ptr<int64_t>();
   p.residual = reinterpret_cast<__nv_bfloat16*>(residual.data_ptr());
@@ -650,8 +648,8 @@ void tp_allreduce_norm(at::Tensor& acc, const std::vector<int64_t>& recv_ptrs,
   p.max_rows = (int)max_rows;
   p.H = (int)acc.size(1);
   p.T = (int)acc.size(0);
+  TORCH_CHECK(algo == 0 || algo == 1, "tp_allreduce_norm: algo 0 (sentinel) or 1 (flags)");
   p.algo = (int)algo;
-  p.sms = b200::num_sms_cached();
   b200::tp_allreduce_norm_launch(p, cur_stream());
   check_launch("tp_allreduce_norm", p.T > 0 ? 1 : 0);
 }

@@ -22,11 +22,11 @@ constexpr int kMaxTP = 8;
 struct TPArNormParams {
   float* acc;                           // local [T][H] fp32 partials (cleared by the kernel)
   long long acc_stride;
-  __nv_bfloat16* recv_peers[kMaxTP];    // per rank: receive slots [2][world][max_rows][H]
-  unsigned int* flag_peers[kMaxTP];     // per rank: flags [2][max_rows][world] (epoch numbers)
-  unsigned int* ctr_peers[kMaxTP];      // per rank: arrival counters [2][kMaxTP] (grid form)
+  __nv_bfloat16* recv_peers[kMaxTP];    // per rank: receive slots [3][world][max_rows][H]
+                                        // (the flag form uses sets 0 and 1)
+  unsigned int* flag_peers[kMaxTP];     // per rank: flags [2][max_rows][world] (flag form)
   unsigned long long* state;            // local: [0] calls completed, [1] CTAs done this call,
-                                        // [2 + parity] CTAs each source has pushed (grid form)
+                                        // [2] rows of the previous call (sentinel form)
   __nv_bfloat16* residual;              // local [T][H], updated in place (all rows)
   long long res_stride;
   const __nv_bfloat16* w;               // RMSNorm weight [H]
@@ -35,8 +35,7 @@ struct TPArNormParams {
   uint32_t* status;
   float eps;
   int rank, world, max_rows, H, T;
-  int algo;  // 0: grid form (all SMs push, one counter per source); 1: one CTA per row
-  int sms;   // SM count of the device (grid size of the grid form)
+  int algo;  // 0: sentinel form (data polled, no flags); 1: per-row flags with fences
 };
 
 void tp_allreduce_norm_launch(const TPArNormParams& p, cudaStream_t stream);

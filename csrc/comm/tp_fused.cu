@@ -181,133 +181,167 @@ __global__ void __launch_bounds__(256) tp_allreduce_norm_kernel(const TPArNormPa
   }
 }
 
-__device__ __forceinline__ void red_release_sys_add_u32(unsigned int* p, unsigned int v) {
-  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// Sentinel form (default).  The receive slots hold the bf16 pattern 0x8000 (negative zero)
+// wherever no data has arrived, so the data is its own flag: a rank stores its partial row
+// straight into every rank's slot [call % 3][this rank][row] (bf16, a partial that rounds to
+// -0.0 is stored as +0.0), and the reader polls its own slots until no half-word of its 16-byte
+// vector is the sentinel -- no memory fence, no flag store, no separate flag round trip.  The
+// slots of the previous call are reset to the sentinel during this call (rows [0, T_prev) of
+// every source, T_prev kept in state[2]); with three slot sets a writer can never reach a set
+// before its reader has reset it (a writer that starts call k + 2 has seen every rank's data
+// of call k + 1, which each rank pushes only after finishing call k, whose kernel reset the
+// set of call k - 1 = k + 2 mod 3).  One CTA per row; every poll is bounded by %globaltimer.
+__device__ __forceinline__ uint4 ld_volatile_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ bool has_sentinel(uint32_t w) {
+  return (w & 0xffffu) == 0x8000u || (w >> 16) == 0x8000u;
+}
+__device__ __forceinline__ uint32_t no_neg_zero(uint32_t w) {
+  if ((w & 0xffffu) == 0x8000u) w &= 0xffff0000u;
+  if ((w >> 16) == 0x8000u) w &= 0x0000ffffu;
+  return w;
 }
 
-// Grid form.  The push is spread over every CTA of the grid (the flattened [T][H] partial in
-// 8-element vectors, grid-stride), so all SMs keep NVLink stores in flight instead of one CTA
-// per row; each CTA then raises one arrival counter per destination rank, counters[parity]
-// [source].  Every CTA waits until all `gridDim.x` CTAs of every source have arrived (the
-// cumulative count per parity is tracked on the device in state[2 + parity], so graph replays
-// and changing T stay consistent: every rank launches the same grid for the same T) and then
-// reduces whole rows, grid-stride, reading the world's bf16 partials from its own receive
-// slots in rank order.  Requires the grid to be co-resident (gridDim.x <= SM count).
 template <int NV>
-__global__ void __launch_bounds__(512) tp_allreduce_norm_grid_kernel(const TPArNormParams p) {
+__global__ void __launch_bounds__(512) tp_allreduce_norm_lamport_kernel(const TPArNormParams p) {
   pdl_trigger();
   pdl_wait();
   __shared__ float red[16];
   __shared__ unsigned long long st_s[2];
   const int tid = threadIdx.x;
+  const int row = blockIdx.x;
   if (tid == 0) {
-    const unsigned long long e0 = *reinterpret_cast<volatile unsigned long long*>(&p.state[0]);
-    st_s[0] = e0;
-    st_s[1] = *reinterpret_cast<volatile unsigned long long*>(&p.state[2 + (e0 & 1ull)]);
+    st_s[0] = *reinterpret_cast<volatile unsigned long long*>(&p.state[0]);
+    st_s[1] = *reinterpret_cast<volatile unsigned long long*>(&p.state[2]);
   }
   __syncthreads();
-  const unsigned int e = (unsigned int)st_s[0];
-  const int par = (int)(e & 1u);
-  const unsigned int target = (unsigned int)st_s[1] + gridDim.x;
-  const int vpr = p.H >> 3;  // 8-element vectors per row
-  const long long nvec = (long long)p.T * vpr;
-  const long long slot_rows = (long long)p.world * p.max_rows;
-  const long long my_slot = ((long long)par * slot_rows + (long long)p.rank * p.max_rows) * p.H;
+  const unsigned long long e = st_s[0];
+  const int T_prev = (int)st_s[1];
+  const int ph = (int)(e % 3ull);
+  const int ph_prev = (ph + 2) % 3;
+  const long long set_elems = (long long)p.world * p.max_rows * p.H;  // one slot set
+  const long long src_elems = (long long)p.max_rows * p.H;             // one source's slot
+  __nv_bfloat16* own = p.recv_peers[p.rank];
 
-  // 1. push: fp32 partial -> bf16, cleared, stored into every rank's slot (own slot included)
-  for (long long v = (long long)blockIdx.x * blockDim.x + tid; v < nvec; v += (long long)gridDim.x * blockDim.x) {
-    const int row = (int)(v / vpr);
-    const int c = (int)(v - (long long)row * vpr) << 3;
-    float4* src = reinterpret_cast<float4*>(p.acc + (long long)row * p.acc_stride + c);
-    const float4 a = src[0], b = src[1];
-    src[0] = make_float4(0.f, 0.f, 0.f, 0.f);
-    src[1] = make_float4(0.f, 0.f, 0.f, 0.f);
-    const uint4 m = make_uint4(pack_bf16x2(a.x, a.y), pack_bf16x2(a.z, a.w), pack_bf16x2(b.x, b.y),
-                               pack_bf16x2(b.z, b.w));
-    const long long off = my_slot + (long long)row * p.H + c;
-    for (int r = 0; r < p.world; ++r) *reinterpret_cast<uint4*>(p.recv_peers[r] + off) = m;
+  // 1. push this row's partial into every rank's slot (own included)
+  const long long my_off = (long long)ph * set_elems + (long long)p.rank * src_elems + (long long)row * p.H;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int idx = (j * 512 + tid) * 8;
+    if (idx < p.H) {
+      float4* src = reinterpret_cast<float4*>(p.acc + (long long)row * p.acc_stride + idx);
+      const float4 a = src[0], b = src[1];
+      src[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+      src[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+      const uint4 m = make_uint4(no_neg_zero(pack_bf16x2(a.x, a.y)), no_neg_zero(pack_bf16x2(a.z, a.w)),
+                                 no_neg_zero(pack_bf16x2(b.x, b.y)), no_neg_zero(pack_bf16x2(b.z, b.w)));
+      for (int r = 0; r < p.world; ++r) *reinterpret_cast<uint4*>(p.recv_peers[r] + my_off + idx) = m;
+    }
   }
-  __threadfence_system();
-  __syncthreads();
-  // 2. one arrival per (CTA, destination), 3. wait for every source's grid
-  if (tid < p.world) red_release_sys_add_u32(p.ctr_peers[tid] + par * kMaxTP + p.rank, 1u);
-  if (tid < p.world) wait_flag(p.ctr_peers[p.rank] + par * kMaxTP + tid, target, p.status, kTimeoutPeerFlag);
-  __syncthreads();
-  // 4. rows, grid-stride: residual += sum of partials (rank order), RMSNorm
-  const __nv_bfloat16* recv = p.recv_peers[p.rank];
-  for (int row = blockIdx.x; row < p.T; row += gridDim.x) {
-    float v[NV][8];
-    float ss = 0.f;
+  // 2. reset the previous call's slot set (rows [0, T_prev) of every source, grid-stride)
+  const uint4 sent = make_uint4(0x80008000u, 0x80008000u, 0x80008000u, 0x80008000u);
+  for (int r = row; r < T_prev; r += gridDim.x) {
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
       const int idx = (j * 512 + tid) * 8;
       if (idx < p.H) {
-        float acc[8];
+        for (int s = 0; s < p.world; ++s)
+          *reinterpret_cast<uint4*>(own + (long long)ph_prev * set_elems + (long long)s * src_elems +
+                                    (long long)r * p.H + idx) = sent;
+      }
+    }
+  }
+  // 3. poll every source's vector until it has fully arrived, sum in rank order
+  bool failed = *reinterpret_cast<volatile uint32_t*>(p.status) != 0u;
+  float v[NV][8];
+  float ss = 0.f;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-        for (int r = 0; r < p.world; ++r) {
-          const uint4 s = __ldcg(reinterpret_cast<const uint4*>(
-              recv + ((long long)par * slot_rows + (long long)r * p.max_rows + row) * p.H + idx));
-          const uint32_t sw[4] = {s.x, s.y, s.z, s.w};
+  for (int j = 0; j < NV; ++j) {
+    const int idx = (j * 512 + tid) * 8;
+    if (idx < p.H) {
+      float acc[8];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float2 f = unpack_bf16x2(sw[i]);
-            acc[2 * i] += f.x;
-            acc[2 * i + 1] += f.y;
+      for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+      for (int s = 0; s < p.world; ++s) {
+        const __nv_bfloat16* q = own + (long long)ph * set_elems + (long long)s * src_elems +
+                                 (long long)row * p.H + idx;
+        uint4 x = ld_volatile_v4(q);
+        if (has_sentinel(x.x) || has_sentinel(x.y) || has_sentinel(x.z) || has_sentinel(x.w)) {
+          const uint64_t t0 = globaltimer_ns();
+          uint32_t n = 0;
+          while (!failed) {
+            x = ld_volatile_v4(q);
+            if (!(has_sentinel(x.x) || has_sentinel(x.y) || has_sentinel(x.z) || has_sentinel(x.w))) break;
+            if ((++n & 63u) == 0 && globaltimer_ns() - t0 > B200_WAIT_TIMEOUT_NS) {
+              set_status(p.status, kTimeoutPeerFlag);
+              failed = true;
+            }
           }
         }
-        __nv_bfloat16* res = p.residual + (long long)row * p.res_stride + idx;
-        const uint4 rv = *reinterpret_cast<const uint4*>(res);
-        const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+        const uint32_t sw[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const float2 f = unpack_bf16x2(rw[i]);
-          v[j][2 * i] = __bfloat162float(__float2bfloat16(acc[2 * i])) + f.x;
-          v[j][2 * i + 1] = __bfloat162float(__float2bfloat16(acc[2 * i + 1])) + f.y;
+          const float2 f = unpack_bf16x2(sw[i]);
+          acc[2 * i] += f.x;
+          acc[2 * i + 1] += f.y;
         }
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          v[j][k] = __bfloat162float(__float2bfloat16(v[j][k]));
-          ss += v[j][k] * v[j][k];
-        }
-        *reinterpret_cast<uint4*>(res) =
-            make_uint4(pack_bf16x2(v[j][0], v[j][1]), pack_bf16x2(v[j][2], v[j][3]),
-                       pack_bf16x2(v[j][4], v[j][5]), pack_bf16x2(v[j][6], v[j][7]));
       }
-    }
-    ss = warp_sum(ss);
-    if ((tid & 31) == 0) red[tid >> 5] = ss;
-    __syncthreads();
-    float t = 0.f;
+      __nv_bfloat16* res = p.residual + (long long)row * p.res_stride + idx;
+      const uint4 rv = *reinterpret_cast<const uint4*>(res);
+      const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
 #pragma unroll
-    for (int w = 0; w < 16; ++w) t += red[w];
-    const float inv = rsqrtf(t / (float)p.H + p.eps);
-#pragma unroll
-    for (int j = 0; j < NV; ++j) {
-      const int idx = (j * 512 + tid) * 8;
-      if (idx < p.H) {
-        const uint4 g = *reinterpret_cast<const uint4*>(p.w + idx);
-        const uint32_t gw[4] = {g.x, g.y, g.z, g.w};
-        uint32_t o[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 f = unpack_bf16x2(gw[i]);
-          o[i] = pack_bf16x2(v[j][2 * i] * inv * f.x, v[j][2 * i + 1] * inv * f.y);
-        }
-        *reinterpret_cast<uint4*>(p.out + (long long)row * p.out_stride + idx) =
-            make_uint4(o[0], o[1], o[2], o[3]);
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = unpack_bf16x2(rw[i]);
+        v[j][2 * i] = __bfloat162float(__float2bfloat16(acc[2 * i])) + f.x;
+        v[j][2 * i + 1] = __bfloat162float(__float2bfloat16(acc[2 * i + 1])) + f.y;
       }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        v[j][k] = __bfloat162float(__float2bfloat16(v[j][k]));
+        ss += v[j][k] * v[j][k];
+      }
+      *reinterpret_cast<uint4*>(res) =
+          make_uint4(pack_bf16x2(v[j][0], v[j][1]), pack_bf16x2(v[j][2], v[j][3]),
+                     pack_bf16x2(v[j][4], v[j][5]), pack_bf16x2(v[j][6], v[j][7]));
     }
-    __syncthreads();  // red[] is reused by the next row
   }
-  // the grid's last CTA advances the call counter and this parity's arrival target
+  ss = warp_sum(ss);
+  if ((tid & 31) == 0) red[tid >> 5] = ss;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int w = 0; w < 16; ++w) t += red[w];
+  const float inv = rsqrtf(t / (float)p.H + p.eps);
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int idx = (j * 512 + tid) * 8;
+    if (idx < p.H) {
+      const uint4 g = *reinterpret_cast<const uint4*>(p.w + idx);
+      const uint32_t gw[4] = {g.x, g.y, g.z, g.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = unpack_bf16x2(gw[i]);
+        o[i] = pack_bf16x2(v[j][2 * i] * inv * f.x, v[j][2 * i + 1] * inv * f.y);
+      }
+      *reinterpret_cast<uint4*>(p.out + (long long)row * p.out_stride + idx) =
+          make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+  // the grid's last CTA advances the call counter and records this call's row count
   if (tid == 0) {
     __threadfence();
     if (atomicAdd(&p.state[1], 1ull) == (unsigned long long)(gridDim.x - 1)) {
       p.state[1] = 0;
-      p.state[2 + par] = (unsigned long long)target;
+      p.state[2] = (unsigned long long)p.T;
       __threadfence();
-      p.state[0] = (unsigned long long)e + 1ull;
+      p.state[0] = e + 1ull;
     }
   }
 }
@@ -335,18 +369,13 @@ void tp_allreduce_norm_launch(const TPArNormParams& p, cudaStream_t stream) {
   if (p.T == 0) return;
   if (p.algo == 0) {
     const int nv = (p.H / 8 + 511) / 512;
-    const long long nvec = (long long)p.T * (p.H / 8);
-    long long g = (nvec + 255) / 256;
-    if (g < p.T) g = p.T;
-    if (g > p.sms) g = p.sms;
-    if (g < 1) g = 1;
-    const dim3 grid((unsigned)g);
+    const dim3 grid(p.T);
     if (nv <= 1)
-      launch_pdl(tp_allreduce_norm_grid_kernel<1>, grid, dim3(512), 0, stream, p);
+      launch_pdl(tp_allreduce_norm_lamport_kernel<1>, grid, dim3(512), 0, stream, p);
     else if (nv <= 2)
-      launch_pdl(tp_allreduce_norm_grid_kernel<2>, grid, dim3(512), 0, stream, p);
+      launch_pdl(tp_allreduce_norm_lamport_kernel<2>, grid, dim3(512), 0, stream, p);
     else if (nv <= 4)
-      launch_pdl(tp_allreduce_norm_grid_kernel<4>, grid, dim3(512), 0, stream, p);
+      launch_pdl(tp_allreduce_norm_lamport_kernel<4>, grid, dim3(512), 0, stream, p);
     else
       throw std::invalid_argument("tp_allreduce_norm: hidden size too large");
     return;

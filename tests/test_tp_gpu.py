@@ -117,7 +117,10 @@ def test_tp2_matches_tp1(ckpt, fused, sp, sdp):
         t = lg[name]
         rel = float((t - r).norm() / r.norm())
         assert rel < 2e-2, (name, rel)
-        assert torch.equal(t.argmax(-1), r.argmax(-1)), name
+        # the same argmax, unless the reference's top two are a near tie (bf16 sums of the
+        # partials in a different order may swap them)
+        gap = r.max(-1).values - r.gather(-1, t.argmax(-1)[:, None]).squeeze(-1)
+        assert bool((gap <= 1e-2 * r.abs().max()).all()), (name, gap)
     # bf16 reduction order differs between TP sizes: require the first tokens to agree and
     # most of the sequence to match.
     same = sum(a == b for r, g2 in zip(ref, got) for a, b in zip(r, g2))

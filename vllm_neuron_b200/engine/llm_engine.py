@@ -244,6 +244,13 @@ class LLMEngine:
         real_group = tp.world > 1 and tp.group is not None
         self.runner = build_runner(args, self.model, self.max_model_len, self.device, self.b200_config)
         self.runner.sampling_dp = bool(self.b200_config.sampling_dp)
+        # accuracy tooling: activation capture / golden replacement (eager steps only)
+        from ..accuracy.tensor_capture import session_from_config
+
+        self.model.capture = session_from_config(self.b200_config.tensor_capture,
+                                                 self.b200_config.tensor_replacement, rank=tp.rank)
+        if self.model.capture is not None:
+            self.runner.use_graphs = False
         dcp = max(1, int(args.decode_context_parallel_size or 1))
         if dcp > 1:
             from ..parallel import state as _ps
@@ -455,7 +462,10 @@ class LLMEngine:
             self._check_device_status()
         now = time.perf_counter()
         finished = self.scheduler.update(out, toks, lps, now=now)
+        cs = getattr(self.model, "capture", None)
         for req in finished:
+            if cs is not None and cs.capture is not None:
+                cs.capture.save(req.request_id)
             if req.slot >= 0 and req.num_pending == 0:
                 self._free_slots.append(req.slot)
                 req.slot = -1

@@ -133,6 +133,8 @@ class LlamaForCausalLM(torch.nn.Module):
         # Hidden states captured after these layers (EAGLE3 drafting): [tokens, len * H]
         self.aux_layers: list[int] = []
         self.aux_hidden: torch.Tensor | None = None
+        # accuracy tooling: activation capture / golden replacement (accuracy.tensor_capture)
+        self.capture = None
 
     # ---------------------------------------------------------------- init / weights
     def _make_attn(self, m, p, layer: int):
@@ -329,6 +331,9 @@ class LlamaForCausalLM(torch.nn.Module):
         fused = small and self.tp_fused is not None
         tp = self.tp
         res, x, Tg = self._embed(b, T, small)
+        cs = self.capture
+        if cs is not None and cs.point("model.embed_tokens", res[:T]):
+            ops.rmsnorm(res[:T], self.layers[0].input_norm, self.eps, out=x[:T])
         nL = len(self.layers)
         for i, ly in enumerate(self.layers):
             k_cache, v_cache = self.kv_caches[i]
@@ -384,6 +389,8 @@ class LlamaForCausalLM(torch.nn.Module):
                 r = b.deep_rows
                 res.index_add_(0, r, b.deep_feats[i].to(res.dtype))
                 x.index_copy_(0, r, ops.rmsnorm(res.index_select(0, r), nxt_norm, self.eps).to(x.dtype))
+            if cs is not None and cs.point(f"model.layers.{i}", res[:T]):
+                ops.rmsnorm(res[:T], nxt_norm, self.eps, out=x[:T])
             if self.aux_layers and i in self.aux_layers:
                 j = self.aux_layers.index(i)
                 self.aux_hidden[:T, j * self.H:(j + 1) * self.H].copy_(res)
@@ -392,9 +399,14 @@ class LlamaForCausalLM(torch.nn.Module):
             self._spf = False
             self.sp_fused.wait_gathered()  # the final norm's rows from every rank
             self.sp_fused.forwards += 1
+        if cs is not None:
+            cs.point("model.norm", x[:T])
         if b.want_hidden:
             return x.index_select(0, b.logits_indices.long())
-        return self.compute_logits(x, b.logits_indices)
+        logits = self.compute_logits(x, b.logits_indices)
+        if cs is not None:
+            cs.point("lm_head", logits, logits=True)
+        return logits
 
     def _gemm_rs_norm(self, a: torch.Tensor, w: torch.Tensor, res: torch.Tensor, norm_w: torch.Tensor) -> torch.Tensor:
         """Fused SP row-parallel epilogue: GEMM reduce-scattered into the owners' slots, then
@@ -426,7 +438,7 @@ class LlamaForCausalLM(torch.nn.Module):
         813-815,1096-1111; nn/embedding.py:236-241)."""
         tp = self.tp
         use_sp = (self.sequence_parallel and tp.world > 1 and not small and b.embed_rows is None
-                  and b.deep_feats is None and not self.aux_layers)
+                  and b.deep_feats is None and not self.aux_layers and self.capture is None)
         if not use_sp:
             self._sp = None
             res = self.ws_residual[:T]

@@ -124,6 +124,9 @@ class Qwen3_5MoeForCausalLM(Qwen3MoeForCausalLM):
                       last_tok=b.last_tok)
         tp.all_reduce_(res)
         ops.rmsnorm(res, self.layers[0].input_norm, self.eps, out=x)
+        cs = self.capture
+        if cs is not None and cs.point("model.embed_tokens", res):
+            ops.rmsnorm(res, self.layers[0].input_norm, self.eps, out=x)
         nL = len(self.layers)
         slots = b.seq_slots
         for i, ly in enumerate(self.layers):
@@ -158,9 +161,16 @@ class Qwen3_5MoeForCausalLM(Qwen3MoeForCausalLM):
             ops.add_rmsnorm(h, res, ly.post_norm, self.eps, out=x)
             nxt_norm = self.layers[i + 1].input_norm if i + 1 < nL else self.final_norm
             self._moe_mlp(ly, x, res, nxt_norm, T)
+            if cs is not None and cs.point(f"model.layers.{i}", res):
+                ops.rmsnorm(res, nxt_norm, self.eps, out=x)
+        if cs is not None:
+            cs.point("model.norm", x)
         if b.want_hidden:
             return x.index_select(0, b.logits_indices.long())
-        return self.compute_logits(x, b.logits_indices)
+        logits = self.compute_logits(x, b.logits_indices)
+        if cs is not None:
+            cs.point("lm_head", logits, logits=True)
+        return logits
 
 
 def _linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor) -> torch.Tensor:

@@ -4,17 +4,18 @@ GEMMs and the RMSNorm (``SPFusedComm``).
 
 ``TPFusedComm`` owns, on every rank of a TP group, one symmetric allocation laid out as
 
-    [ receive slots: 2 x world x max_rows x H bf16 | flags: 2 x max_rows x world u32 |
-      arrival counters: 2 x 8 u32 ]
+    [ receive slots: 3 x world x max_rows x H bf16 | flags: 2 x max_rows x world u32 ]
 
 mapped on every peer through CUDA IPC.  ``allreduce_norm`` finishes a row-parallel
 projection (``o_proj`` / ``down_proj``) whose local split-K GEMM accumulated fp32 partial sums:
-one kernel pushes the bf16 partials into every peer's receive slots (spread over every SM of
-the grid), raises one arrival counter per (CTA, destination), waits for every source's grid
-and computes ``residual += sum(partials)`` in rank order followed by RMSNorm, so every rank
-ends with the same normalized activation for the next column-parallel GEMM.  ``algo = 1``
-selects the older one-CTA-per-row form with per-row flags (kept for comparison).  This is the
-B200 replacement of ``RowParallelLinear`` + all-reduce + residual + norm (reference:
+one kernel stores each bf16 partial row into every rank's receive slot and computes
+``residual += sum(partials)`` in rank order followed by RMSNorm, so every rank ends with the same
+normalized activation for the next column-parallel GEMM.  The slots hold the bf16 sentinel
+0x8000 (negative zero) where no data has arrived, so the reader polls the data itself -- no
+fence and no flag round trip per call (three slot sets rotate; each call resets the previous
+call's set).  ``algo = 1`` selects the older form (per-row flags raised after a system-scope
+fence, two slot sets), kept for comparison; one object must keep one form.  This is the B200
+replacement of ``RowParallelLinear`` + all-reduce + residual + norm (reference:
 vllm_neuron/nn/rpl.py:23-154; all-reduce sites vllm_neuron/model/llama3/model.py:989,1113).
 """
 from __future__ import annotations
@@ -28,17 +29,16 @@ from .comm import GroupComm
 
 class TPFusedComm:
     def __init__(self, tp: GroupComm, hidden: int, max_rows: int, device: torch.device,
-                 cpu_group=None):
-        assert 1 < tp.world <= 8
+                 cpu_group=None, algo: int = 0):
+        assert 1 < tp.world <= 8 and algo in (0, 1)
         self.tp = tp
         self.W, self.rank = tp.world, tp.rank
         self.H = hidden
         self.max_rows = max_rows
         self.device = device
-        slot_bytes = 2 * self.W * max_rows * hidden * 2
+        slot_bytes = 3 * self.W * max_rows * hidden * 2
         self.off_flags = _align(slot_bytes)
-        self.off_ctr = self.off_flags + _align(2 * max_rows * self.W * 4)
-        total = self.off_ctr + _align(2 * 8 * 4)
+        total = self.off_flags + _align(2 * max_rows * self.W * 4)
         with torch.cuda.device(device):
             ptr, handle = ext().symm_alloc(total)
         self._local = ptr
@@ -57,19 +57,20 @@ class TPFusedComm:
                     self._opened.append(p)
         self.recv_ptrs = list(self.peers)
         self.flag_ptrs = [p + self.off_flags for p in self.peers]
-        self.ctr_ptrs = [p + self.off_ctr for p in self.peers]
-        # [0] calls completed, [1] CTAs finished in the running call, [2 + parity] arrivals
-        # per source so far (grid form)
+        # [0] calls completed, [1] CTAs finished in the running call, [2] rows of the last call
         self.state = torch.zeros(4, dtype=torch.int64, device=device)
-        # 0: grid form (every SM pushes; one arrival counter per source), 1: one CTA per row
-        self.algo = 0
+        self.algo = algo
+        if algo == 0:  # every slot starts as the "not arrived" sentinel
+            dev = device.index if device.index is not None else torch.cuda.current_device()
+            ext().tensor_from_ptr(ptr, [slot_bytes // 2], torch.bfloat16, dev).fill_(-0.0)
+            torch.cuda.synchronize(device)
         dist.barrier(group=cpu_group)
 
     def allreduce_norm(self, acc: torch.Tensor, residual: torch.Tensor, norm_w: torch.Tensor,
                        eps: float, out: torch.Tensor) -> torch.Tensor:
         """``residual += all_reduce(acc)``; ``out = rmsnorm(residual) * norm_w``; clears ``acc``."""
-        ext().tp_allreduce_norm(acc, self.recv_ptrs, self.flag_ptrs, self.ctr_ptrs, self.state, residual,
-                                norm_w, out, eps, self.rank, self.max_rows, self.algo)
+        ext().tp_allreduce_norm(acc, self.recv_ptrs, self.flag_ptrs, self.state, residual, norm_w, out,
+                                eps, self.rank, self.max_rows, self.algo)
         return out
 
     def close(self):

@@ -608,6 +608,7 @@ class ModelRunner:
             fb, samp = self._views(dev, lay, B, S, W, decode, splits)
             fb.work = fb.work[:W]
             self._attach_prompt_embeds(out, fb)
+            self._begin_capture(out)
             if S > 0:
                 mask = bitmask.to(self.device, non_blocking=True) if bitmask is not None else None
                 self._forward_and_sample(fb, samp, S, self.tok_dev, self.lp_dev, mask)
@@ -648,10 +649,30 @@ class ModelRunner:
         fb.work = fb.work[:W]
         self._attach_prompt_embeds(out, fb)
         fb.want_hidden = hidden
+        self._begin_capture(out)
         logits = self.model.forward(fb).clone()
         if self.is_cuda:
             torch.cuda.synchronize(self.device)
         return logits
+
+    def _begin_capture(self, out: SchedulerOutput):
+        """Tell the model's capture session (accuracy tooling) which request and positions each
+        row of this step holds."""
+        cs = getattr(self.model, "capture", None)
+        if cs is None:
+            return
+        from ..accuracy.tensor_capture import RowGroup, prompt_key
+
+        groups, lgroups, row, lrow = [], [], 0, 0
+        for s in out.scheduled:
+            key = prompt_key(s.req.prompt_token_ids)
+            groups.append(RowGroup(s.req.request_id, key, s.start, s.num_tokens, row))
+            row += s.num_tokens
+            nl = s.num_logits
+            if nl:
+                lgroups.append(RowGroup(s.req.request_id, key, s.start + s.num_tokens - nl, nl, lrow))
+                lrow += nl
+        cs.begin(groups, lgroups)
 
     def execute(self, out: SchedulerOutput, want_logprobs: bool = False) -> tuple[np.ndarray, np.ndarray | None]:
         """Run one step synchronously; returns sampled tokens (and logprobs) in row order."""
