@@ -10,6 +10,7 @@
 #include <unordered_map>
 
 #include "attn/attention.h"
+#include "comm/ep_fused.h"
 #include "comm/symm_mem.h"
 #include "gemm/gemm.h"
 #include "misc/misc.h"
@@ -654,6 +655,82 @@ void tp_allreduce_norm(at::Tensor& acc, const std::vector<int64_t>& recv_ptrs,
   check_launch("tp_allreduce_norm", p.T > 0 ? 1 : 0);
 }
 
+// ------------------------------------------------------------------------- EP exchange
+// One stage of the device-side expert-parallel exchange (ep_fused.cu): 0 dispatch, 1 receive,
+// 2 return, 3 combine.  `offs` = byte offsets (ctrl, rows, ids, w, src, comb) of the symmetric
+// layout, `dims` = (rank, world, H, k, num_experts, e_local, tokens_cap, rows_cap, T).
+void ep_exchange(int64_t stage, const std::vector<int64_t>& peers, const std::vector<int64_t>& offs,
+                 const std::vector<int64_t>& dims, c10::optional<at::Tensor> x,
+                 c10::optional<at::Tensor> topk_ids, c10::optional<at::Tensor> topk_w,
+                 c10::optional<at::Tensor> out, c10::optional<at::Tensor> y, at::Tensor& recv_count,
+                 at::Tensor& ctas_done, at::Tensor& state) {
+  TORCH_CHECK(offs.size() == 6 && dims.size() == 9, "ep_exchange: bad layout arguments");
+  TORCH_CHECK(peers.size() == (size_t)dims[1] && dims[1] <= b200::kMaxEP, "ep_exchange: peers");
+  CHECK_CUDA(recv_count);
+  TORCH_CHECK(recv_count.scalar_type() == at::kInt && ctas_done.scalar_type() == at::kInt &&
+                  state.scalar_type() == at::kLong, "ep_exchange: control tensor dtypes");
+  const c10::cuda::CUDAGuard guard(recv_count.device());
+  b200::EPExchangeParams p{};
+  for (size_t r = 0; r < peers.size(); ++r) p.peers[r] = (void*)peers[r];
+  p.off_ctrl = offs[0];
+  p.off_rows = offs[1];
+  p.off_ids = offs[2];
+  p.off_w = offs[3];
+  p.off_src = offs[4];
+  p.off_comb = offs[5];
+  p.rank = (int)dims[0];
+  p.world = (int)dims[1];
+  p.H = (int)dims[2];
+  p.k = (int)dims[3];
+  p.num_experts = (int)dims[4];
+  p.e_local = (int)dims[5];
+  p.tokens_cap = (int)dims[6];
+  p.rows_cap = (int)dims[7];
+  p.T = (int)dims[8];
+  p.recv_count = recv_count.data_ptr<int>();
+  p.ctas_done = reinterpret_cast<unsigned int*>(ctas_done.data_ptr<int>());
+  p.state = (unsigned long long*)state.data_ptr<int64_t>();
+  p.status = status_word();
+  if (stage == 0 || stage == 3) {
+    TORCH_CHECK(topk_ids.has_value() && topk_ids->scalar_type() == at::kInt && topk_ids->is_contiguous() &&
+                    topk_ids->size(-1) == p.k && topk_ids->size(0) >= p.T,
+                "ep_exchange: topk_ids int32 [T, k]");
+    p.topk_ids = topk_ids->data_ptr<int>();
+  }
+  if (stage == 0) {
+    TORCH_CHECK(x.has_value() && topk_w.has_value(), "ep_exchange: dispatch needs x and weights");
+    CHECK_BF16(x.value());
+    TORCH_CHECK(x->stride(1) == 1 && x->stride(0) % 8 == 0 && x->size(1) == p.H && x->size(0) >= p.T,
+                "ep_exchange: x [T, H]");
+    TORCH_CHECK(topk_w->scalar_type() == at::kFloat && topk_w->is_contiguous(), "ep_exchange: weights");
+    p.x = reinterpret_cast<const __nv_bfloat16*>(x->data_ptr());
+    p.ldx = x->stride(0);
+    p.topk_w = topk_w->data_ptr<float>();
+    b200::ep_dispatch_launch(p, cur_stream());
+  } else if (stage == 1) {
+    b200::ep_recv_launch(p, cur_stream());
+  } else if (stage == 2) {
+    TORCH_CHECK(y.has_value(), "ep_exchange: return needs y");
+    CHECK_BF16(y.value());
+    TORCH_CHECK(y->stride(1) == 1 && y->stride(0) % 8 == 0 && y->size(1) == p.H && y->size(0) >= p.rows_cap,
+                "ep_exchange: y [rows_cap, H]");
+    p.y = reinterpret_cast<const __nv_bfloat16*>(y->data_ptr());
+    p.ldy = y->stride(0);
+    b200::ep_return_launch(p, cur_stream());
+  } else if (stage == 3) {
+    TORCH_CHECK(out.has_value(), "ep_exchange: combine needs out");
+    CHECK_BF16(out.value());
+    TORCH_CHECK(out->stride(1) == 1 && out->stride(0) % 8 == 0 && out->size(1) == p.H && out->size(0) >= p.T,
+                "ep_exchange: out [T, H]");
+    p.out = reinterpret_cast<__nv_bfloat16*>(out->data_ptr());
+    p.ldo = out->stride(0);
+    b200::ep_combine_launch(p, cur_stream());
+  } else {
+    TORCH_CHECK(false, "ep_exchange: stage 0..3");
+  }
+  check_launch("ep_exchange");
+}
+
 // ------------------------------------------------------------------------------ MoE
 // out[rows of expert e] = x_perm[rows] @ w[e]^T for the tile list written by moe_align.
 // x_perm [R, K] bf16 (expert-sorted rows), w [E_local, N, K] bf16, out [R, N] (bf16) with the
@@ -999,6 +1076,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tensor_from_ptr", &tensor_from_ptr);
   m.def("tp_allreduce_norm", &tp_allreduce_norm);
   m.def("gemm_w8", &gemm_w8);
+  m.def("ep_exchange", &ep_exchange);
   m.def("gemm_grouped", &gemm_grouped);
   m.def("moe_route", &moe_route);
   m.def("moe_align", &moe_align);

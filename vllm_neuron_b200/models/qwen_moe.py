@@ -63,9 +63,26 @@ class MoEMixin:
     def _post_init_moe(self):
         self.e_start = self.a2a.e_start if self.a2a is not None else self.tp.rank * self.e_local
         self.moe_ws = None
+        self.ep_fused = None
         if self.device.type == "cuda":
             self.moe_ws = M.MoEWorkspace.create(self.max_tokens + self.tp.world, self.topk, self.E, self.e_local, self.H,
                                                 self.I_moe, self.device, shared_inter=self.I_sh)
+            from .. import envs
+
+            if self.a2a is not None and not envs.VLLM_B200_DISABLE_FUSED_COMM:
+                # wide EP on the GPU: the device-side exchange over NVLink peer memory
+                from ..parallel import state as ps
+                from ..parallel.ep_fused import EPFusedExchange
+
+                st = ps.get_parallel_state()
+                cap = self.max_tokens + self.tp.world
+                self.ep_fused = EPFusedExchange(st.ep.group, st.ep.rank, st.ep.world, self.E, self.topk,
+                                                self.H, cap, self.device, st.cpu)
+                R = self.ep_fused.rows_cap
+                self.ep_ws = M.MoEWorkspace.create(R, self.topk, self.E, self.e_local, self.H, self.I_moe,
+                                                   self.device)
+                self.ep_y = torch.zeros(R, self.H, dtype=torch.bfloat16, device=self.device)
+                self.ep_out = torch.zeros(cap, self.H, dtype=torch.bfloat16, device=self.device)
 
     def _moe_params(self, m, p):
         m.router = p(self.E + (1 if self.I_sh and self.shared_gated else 0), self.H)
@@ -107,11 +124,22 @@ class MoEMixin:
         gated = sh_gu is not None and self.shared_gated
         ids, w = M.route(logits, self.topk, self.route_mode, self.renorm, getattr(ly, "router_bias", None),
                          num_experts=E, scale=self.routed_scale)
-        plan, rows, aff = self.a2a.dispatch(x, ids, w)
-        lids, lw = EP.local_routing(aff, self.e_start, self.topk)
-        part = M.moe_experts(rows, lids, lw, ly.w_gu, ly.w_down, b_gu, b_down, self.expert_act, alpha,
-                             limit, e_start=self.e_start)
-        y = self.a2a.combine(part, plan).float()
+        if x.is_cuda and self.ep_fused is not None:
+            # device-side exchange: rows land in this rank's receive buffer, the experts run on
+            # its static row bound, reduced rows go back into the owners' combine slots
+            ex = self.ep_fused
+            ex.dispatch(x, ids, w)
+            rows, rids, rw = ex.recv()
+            M._experts_cuda(rows, rids, rw, ly.w_gu, ly.w_down, self.topk, b_gu, b_down, self.expert_act,
+                            alpha, limit, self.e_start, self.ep_ws, self.ep_y, None, None, None, None, 0)
+            ex.ret(self.ep_y)
+            y = ex.combine(self.ep_out[:x.shape[0]]).float()
+        else:
+            plan, rows, aff = self.a2a.dispatch(x, ids, w)
+            lids, lw = EP.local_routing(aff, self.e_start, self.topk)
+            part = M.moe_experts(rows, lids, lw, ly.w_gu, ly.w_down, b_gu, b_down, self.expert_act, alpha,
+                                 limit, e_start=self.e_start)
+            y = self.a2a.combine(part, plan).float()
         if sh_gu is not None:
             if x.is_cuda:
                 from ..ops.activation import silu_mul
