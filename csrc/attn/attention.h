@@ -49,6 +49,9 @@ struct PagedAttnParams {
   // Write unnormalised split partials (part_o / part_lse) even for one split and leave the
   // merge to the caller (DCP merges the partials of all ranks after exchanging them).
   int partial_out;
+  // Packed query rows per prefill work item: 64 (mma.sync kernel) or 128 (tcgen05 kernel,
+  // fmha_sm100.cu); 0 means 64.  The work list must have been built with the same value.
+  int prefill_rows;
 };
 
 #ifdef __CUDACC__
@@ -68,6 +71,11 @@ __device__ __forceinline__ int dcp_last_visible(int g, int bs, int size, int ran
 
 void paged_attention_launch(const PagedAttnParams& p, int num_work, int head_dim, bool decode,
                             cudaStream_t stream);
+
+// tcgen05 prefill attention (fmha_sm100.cu): head_dim 128, bf16 cache, one split, 128-row work
+// items.
+bool fmha_prefill_supported(const PagedAttnParams& p, int head_dim);
+void fmha_prefill_launch(const PagedAttnParams& p, int num_work, cudaStream_t stream);
 
 // Persistent TMA-fed decode kernel (paged_decode.cu); used for decode batches when the caches
 // are contiguous [num_blocks, Hkv, block_size, D] tensors with block_size % 16 == 0 and a

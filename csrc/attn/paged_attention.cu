@@ -39,6 +39,17 @@ namespace {
 constexpr int kKvTile = 64;
 constexpr float kLog2e = 1.4426950408889634f;
 
+// A block id at or beyond the cache's block count (kv_rows / (Hkv * block_size), when known)
+// is replaced by the null block 0 and reported as kBadIndex in the status word, so a corrupt
+// block table cannot make the kernel read outside the cache.
+__device__ __forceinline__ int checked_block(const PagedAttnParams& p, int blk) {
+  if (p.kv_rows > 0 && (blk < 0 || (long long)(blk + 1) * p.Hkv * p.block_size > p.kv_rows)) {
+    set_status(p.status, kBadIndex);
+    return 0;
+  }
+  return blk;
+}
+
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool pred) {
   const int n = pred ? 16 : 0;
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)),
@@ -167,7 +178,7 @@ __global__ void __launch_bounds__(128)
         const bool valid = tok < kv_len;
         const int page = valid ? tok / p.block_size : 0;
         const int slot = tok - page * p.block_size;
-        const int blk = valid ? p.block_tables[(long long)b * p.bt_stride + page] : 0;
+        const int blk = valid ? checked_block(p, p.block_tables[(long long)b * p.bt_stride + page]) : 0;
         const long long off = (long long)blk * p.kv_block_stride +
                               ((long long)kvh * p.block_size + slot) * D + c * 16;
         uint4 kr = make_uint4(0u, 0u, 0u, 0u), vr = kr;
@@ -196,7 +207,7 @@ __global__ void __launch_bounds__(128)
       const bool valid = tok < kv_len;
       const int page = valid ? tok / p.block_size : 0;
       const int slot = tok - page * p.block_size;
-      const int blk = valid ? p.block_tables[(long long)b * p.bt_stride + page] : 0;
+      const int blk = valid ? checked_block(p, p.block_tables[(long long)b * p.bt_stride + page]) : 0;
       const long long off = (long long)blk * p.kv_block_stride +
                             ((long long)kvh * p.block_size + slot) * D + c * 8;
       cp_async16(sK + stage * TILE_BYTES + swz<D>(r, c), p.k_cache + off, valid);
@@ -576,6 +587,15 @@ void paged_attention_launch(const PagedAttnParams& p_in, int num_work, int head_
   const bool tma = decode && paged_decode_tma_supported(p, head_dim);
   // device split factors are a feature of the TMA decode path with the warp combine (<= 32)
   if (!tma || p.num_splits > 32 || p.partial_out) p.splits_dev = nullptr;
+  if (!decode && p.prefill_rows == 128) {
+    if (!fmha_prefill_supported(p, head_dim))
+      throw std::invalid_argument("paged_attention: 128-row prefill work needs the tcgen05 kernel's "
+                                  "conditions (head_dim 128, bf16 cache, one split, no DCP)");
+    fmha_prefill_launch(p, num_work, stream);
+    return;
+  }
+  if (!decode && p.prefill_rows != 0 && p.prefill_rows != 64)
+    throw std::invalid_argument("paged_attention: prefill work items must hold 64 or 128 rows");
   if (tma) {
     paged_decode_tma_launch(p, num_work, head_dim, stream);
   } else if (head_dim == 128) {

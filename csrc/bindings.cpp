@@ -342,7 +342,7 @@ void paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::T
                      c10::optional<at::Tensor> sinks, int64_t num_splits, int64_t num_kv_heads,
                      int64_t window, double scale, bool decode, double k_scale, double v_scale,
                      c10::optional<at::Tensor> splits_dev, c10::optional<at::Tensor> dcp_seq_lens,
-                     int64_t dcp_size, int64_t dcp_rank, bool partial_out) {
+                     int64_t dcp_size, int64_t dcp_rank, bool partial_out, int64_t prefill_rows) {
   CHECK_CUDA(q);
   CHECK_BF16(q);
   const bool fp8 = k_cache.scalar_type() == at::kFloat8_e4m3fn;
@@ -374,6 +374,7 @@ void paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::T
   p.o_stride_t = out.stride(0);
   p.num_splits = (int)num_splits;
   p.partial_out = partial_out ? 1 : 0;
+  p.prefill_rows = (int)prefill_rows;
   if (num_splits > 1 || partial_out) {
     TORCH_CHECK(part_o.has_value() && part_lse.has_value(), "split-KV needs partial buffers");
     TORCH_CHECK(part_o->scalar_type() == at::kFloat && part_lse->scalar_type() == at::kFloat,
@@ -408,7 +409,8 @@ void paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::T
   }
   p.total_tokens = (int)q.size(0);
   p.status = status_word();
-  if (decode && k_cache.is_contiguous() && v_cache.is_contiguous()) {
+  if (k_cache.is_contiguous() && v_cache.is_contiguous()) {
+    // rows of the caches: the TMA maps' extent and the kernels' block-id bound
     p.kv_rows = k_cache.size(0) * k_cache.size(1) * k_cache.size(2);
     p.sched = decode_sched_words();
   }
@@ -484,6 +486,8 @@ void rope_kv_write(at::Tensor& qkv, const at::Tensor& positions,
     p.v_cache = reinterpret_cast<__nv_bfloat16*>(v_cache->data_ptr());
     p.kv_block_stride = k_cache->stride(0);
     p.block_size = (int)k_cache->size(2);
+    p.num_blocks = k_cache->size(0);
+    p.status = status_word();
     const bool fp8 = k_cache->scalar_type() == at::kFloat8_e4m3fn;
     TORCH_CHECK(fp8 || k_cache->scalar_type() == at::kBFloat16,
                 "rope_kv_write: cache must be bfloat16 or float8_e4m3fn");

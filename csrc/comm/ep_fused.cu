@@ -58,7 +58,7 @@ __device__ bool wait_eq(const unsigned int* f, unsigned int target, uint32_t* st
   while (true) {
     if (*reinterpret_cast<volatile uint32_t*>(status) != 0u) return false;
     if (ld_acquire_u32(f) == target) return true;
-    if (globaltimer_ns() - t0 > B200_WAIT_TIMEOUT_NS) {
+    if (globaltimer_ns() - t0 > B200_PEER_TIMEOUT_NS) {
       set_status(status, kTimeoutPeerFlag);
       return false;
     }

@@ -40,7 +40,7 @@ __device__ __forceinline__ bool wait_ctr(const unsigned int* c, unsigned int tar
   if (status != nullptr && *reinterpret_cast<volatile uint32_t*>(status) != 0u) return false;
   const uint64_t t0 = globaltimer_ns();
   while ((int)(ld_acq_sys(c) - target) < 0) {
-    if (globaltimer_ns() - t0 > B200_WAIT_TIMEOUT_NS) {
+    if (globaltimer_ns() - t0 > B200_PEER_TIMEOUT_NS) {
       set_status(status, kTimeoutPeerFlag);
       return false;
     }

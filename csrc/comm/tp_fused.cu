@@ -43,7 +43,7 @@ __device__ __forceinline__ void st_release_sys_u32(unsigned int* p, unsigned int
 // once when an earlier wait already failed (status word set: fail fast, peers out of step).
 __device__ __forceinline__ bool wait_flag(const unsigned int* f, unsigned int target,
                                           uint32_t* status, uint32_t code,
-                                          uint64_t timeout_ns = B200_WAIT_TIMEOUT_NS) {
+                                          uint64_t timeout_ns = B200_PEER_TIMEOUT_NS) {
   if ((int)(ld_acquire_sys_u32(f) - target) >= 0) return true;
   if (status != nullptr && *reinterpret_cast<volatile uint32_t*>(status) != 0u) return false;
   const uint64_t t0 = globaltimer_ns();
@@ -278,7 +278,7 @@ __global__ void __launch_bounds__(512) tp_allreduce_norm_lamport_kernel(const TP
           while (!failed) {
             x = ld_volatile_v4(q);
             if (!(has_sentinel(x.x) || has_sentinel(x.y) || has_sentinel(x.z) || has_sentinel(x.w))) break;
-            if ((++n & 63u) == 0 && globaltimer_ns() - t0 > B200_WAIT_TIMEOUT_NS) {
+            if ((++n & 63u) == 0 && globaltimer_ns() - t0 > B200_PEER_TIMEOUT_NS) {
               set_status(p.status, kTimeoutPeerFlag);
               failed = true;
             }

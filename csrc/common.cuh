@@ -18,6 +18,13 @@
 #ifndef B200_WAIT_TIMEOUT_NS
 #define B200_WAIT_TIMEOUT_NS 2000000000ull  // 2 s: far above any legitimate wait
 #endif
+// Waits on another rank (peer flags, counters, sentinel slots) also absorb the host-side skew
+// between the ranks' processes -- a rank that loads a kernel module for the first time or
+// prepares a large step on the host can trail its peers by seconds -- so they get a longer
+// budget.  A failed peer is still reported, after this time instead of 2 s.
+#ifndef B200_PEER_TIMEOUT_NS
+#define B200_PEER_TIMEOUT_NS 20000000000ull  // 20 s
+#endif
 
 namespace b200 {
 

@@ -40,6 +40,10 @@ struct RopeKvParams {
   // satfinite(v * v_inv_scale).
   int kv_fp8;
   float k_inv_scale, v_inv_scale;
+  // Bounds guard: slots at or beyond num_blocks * block_size are not written and raise kBadIndex
+  // in the status word (0: unchecked).
+  long long num_blocks;
+  uint32_t* status;
 };
 void rope_kv_write_launch(const RopeKvParams& p, void* qkv, bool qkv_is_f32, int T,
                           cudaStream_t stream);

@@ -292,6 +292,8 @@ __global__ void __launch_bounds__(256) rope_kv_write_kernel(const RopeKvParams p
                            : 1.f;
 #pragma unroll
       for (int e = 0; e < PER; ++e) dst[lane + 32 * e] = __float2bfloat16(v[e] * qs);
+    } else if (slot >= 0 && p.num_blocks > 0 && slot >= p.num_blocks * p.block_size) {
+      if (lane == 0) set_status(p.status, kBadIndex);  // slot past the cache: not written
     } else if (slot >= 0) {
       const int kvh = is_k ? h - p.Hq : h - p.Hq - p.Hkv;
       const long long blk = slot / p.block_size, off = slot % p.block_size;

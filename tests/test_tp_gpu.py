@@ -121,8 +121,8 @@ def test_tp2_matches_tp1(ckpt, fused, sp, sdp):
         # partials in a different order may swap them)
         gap = r.max(-1).values - r.gather(-1, t.argmax(-1)[:, None]).squeeze(-1)
         assert bool((gap <= 1e-2 * r.abs().max()).all()), (name, gap)
-    # bf16 reduction order differs between TP sizes: require the first tokens to agree and
-    # most of the sequence to match.
+    # The first generated token is the argmax of the "long" logits checked above (near ties
+    # may swap); bf16 reduction order differs between TP sizes, so afterwards require most of
+    # the generated tokens to match.
     same = sum(a == b for r, g2 in zip(ref, got) for a, b in zip(r, g2))
-    assert all(r[0] == g2[0] for r, g2 in zip(ref, got)), (ref, got)
     assert same >= 0.8 * sum(len(r) for r in ref), (ref, got)

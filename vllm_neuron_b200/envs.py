@@ -65,6 +65,8 @@ _flag("KV_CACHE_MAX_GIB", _float, None, "cap of the KV-cache budget per GPU (GiB
 _flag("MIN_KV_BUDGET_GIB", _float, 0.0, "refuse to start when the KV budget is below this (GiB)")
 _flag("SKIP_WARMUP", _bool, False, "skip the warm-up passes at start-up")
 _flag("DISABLE_CUDA_GRAPHS", _bool, False, "run decode eagerly (no CUDA-graph capture)")
+_flag("DISABLE_TC_ATTENTION", _bool, False,
+      "run prefill attention on the mma.sync kernel instead of the tcgen05 kernel")
 _flag("DISABLE_FUSED_COMM", _bool, False,
       "use NCCL collectives instead of the fused peer-memory kernels for TP communication")
 _flag("FP4_DECODE_MAX_TOKENS", _int, 64,

@@ -62,6 +62,7 @@ class ForwardBatch:
     max_q_len: int = 0                       # longest query of the step (host value; 0 = unknown)
     splits_dev: torch.Tensor | None = None   # [1] int32 split-KV factor of this decode step
     seq_lens_local: torch.Tensor | None = None  # [B] int32 tokens held by this DCP rank
+    prefill_rows: int = 64                   # packed query rows per prefill work item (64 / 128)
 
 
 def _shard(n: int, world: int, rank: int) -> tuple[int, int]:
@@ -541,7 +542,8 @@ class LlamaForCausalLM(torch.nn.Module):
         ops.paged_attention(q.view(T, self.Hq, self.D), k_cache, v_cache, b.block_tables, b.seq_lens,
                             b.q_start, b.work, b.decode, ns, self.scale, window=window, sinks=sinks,
                             out=attn.view(T, self.Hq, self.D), part_o=part_o, part_lse=part_l,
-                            k_scale=kv_scale[0], v_scale=kv_scale[1], splits_dev=b.splits_dev)
+                            k_scale=kv_scale[0], v_scale=kv_scale[1], splits_dev=b.splits_dev,
+                            prefill_rows=b.prefill_rows)
 
     def _attention_dcp(self, q, attn, k_cache, v_cache, b: ForwardBatch,
                        kv_scale: tuple[float, float]):

@@ -24,7 +24,23 @@ from ._ext import ext
 
 FP8_MAX = 448.0   # largest finite float8_e4m3fn value
 PREFILL_ROWS = 64
+PREFILL_ROWS_TC = 128  # work items of the tcgen05 prefill kernel (csrc/attn/fmha_sm100.cu)
 DECODE_ROWS = 16
+
+
+def prefill_rows(head_dim: int, kv_dtype, block_size: int = 16, group: int = 1, dcp_size: int = 1) -> int:
+    """Packed query rows per prefill work item: 128 when the tcgen05 kernel serves the step
+    (head_dim 128, bf16 cache, block size dividing its 64-token KV tile, GQA group dividing 128,
+    no DCP), else 64 for the mma.sync kernel.  The work list and the kernel must agree."""
+    import torch
+
+    from .. import envs
+
+    if (head_dim == 128 and kv_dtype == torch.bfloat16 and dcp_size <= 1 and block_size > 0
+            and block_size % 8 == 0 and 64 % block_size == 0 and group > 0 and 128 % group == 0
+            and not envs.VLLM_B200_DISABLE_TC_ATTENTION):
+        return PREFILL_ROWS_TC
+    return PREFILL_ROWS
 KV_TILE = 64
 DECODE_TILE = 16   # tokens per TMA tile of the decode kernel
 DECODE_WARPS = 8   # persistent warps per SM of the decode kernel
@@ -40,7 +56,8 @@ class AttnWork:
 
 
 def build_work(q_lens: np.ndarray, seq_lens: np.ndarray, group: int, num_kv_heads: int,
-               num_sms: int = 148, max_splits: int = 16, head_dim: int = 128) -> AttnWork:
+               num_sms: int = 148, max_splits: int = 16, head_dim: int = 128,
+               prefill_rows: int = PREFILL_ROWS) -> AttnWork:
     """Split the batch into CTA work items.
 
     Decode mode is used when every sequence has at most ``DECODE_ROWS`` packed rows
@@ -62,11 +79,11 @@ def build_work(q_lens: np.ndarray, seq_lens: np.ndarray, group: int, num_kv_head
         return AttnWork(work.astype(np.int32), True, splits)
     seqs, starts = [], []
     for b, r in enumerate(rows):
-        n = int(math.ceil(r / PREFILL_ROWS))
+        n = int(math.ceil(r / prefill_rows))
         # Longest-first ordering is applied by sorting work items by remaining KV length.
         for t in range(n):
             seqs.append(b)
-            starts.append(t * PREFILL_ROWS)
+            starts.append(t * prefill_rows)
     work = np.stack([np.asarray(seqs, dtype=np.int64), np.asarray(starts, dtype=np.int64)], 1) \
         if seqs else np.zeros((0, 2), dtype=np.int64)
     if len(work):
@@ -82,7 +99,8 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
                     window: int = 0, sinks: torch.Tensor | None = None,
                     out: torch.Tensor | None = None, part_o: torch.Tensor | None = None,
                     part_lse: torch.Tensor | None = None, k_scale: float = 1.0,
-                    v_scale: float = 1.0, splits_dev: torch.Tensor | None = None) -> torch.Tensor:
+                    v_scale: float = 1.0, splits_dev: torch.Tensor | None = None,
+                    prefill_rows: int = PREFILL_ROWS) -> torch.Tensor:
     """Attention of ``q [T, Hq, D]`` over the paged cache; returns ``out [T, Hq, D]``.
 
     A ``torch.float8_e4m3fn`` cache holds ``K / k_scale`` and ``V / v_scale`` (per-tensor
@@ -103,7 +121,8 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
         part_lse = torch.empty((num_splits, T, Hq), dtype=torch.float32, device=q.device)
     ext().paged_attention(q, k_cache, v_cache, block_tables, seq_lens, q_start, work, out,
                           part_o, part_lse, sinks, num_splits, k_cache.shape[1], window, scale,
-                          decode, float(k_scale), float(v_scale), splits_dev, None, 1, 0, False)
+                          decode, float(k_scale), float(v_scale), splits_dev, None, 1, 0, False,
+                          0 if decode else int(prefill_rows))
     return out
 
 
@@ -144,7 +163,7 @@ def paged_attention_partial(q: torch.Tensor, k_cache: torch.Tensor, v_cache: tor
     ext().paged_attention(q, k_cache, v_cache, block_tables, seq_lens, q_start, work, q,
                           part_o, part_lse, None, num_splits, k_cache.shape[1], 0, scale,
                           decode, float(k_scale), float(v_scale), None, dcp_seq_lens,
-                          int(dcp_size), int(dcp_rank), True)
+                          int(dcp_size), int(dcp_rank), True, 0)
 
 
 def attn_combine(part_o: torch.Tensor, part_lse: torch.Tensor,

@@ -127,6 +127,26 @@ class B200Platform(Platform):
             raise ValueError(f"quantization {quant!r} is not served by the B200 platform "
                              f"(supported: {cls.supported_quantization})")
 
+    @classmethod
+    def validate_request(cls, processed_inputs, params) -> None:
+        """Refuse what the worker cannot serve before the request reaches the scheduler
+        (reference: NeuronPlatform.validate_request, vllm/platform.py:446-485): pooling requests
+        (the worker generates only), prompt logprobs, and top-k logprob lists beyond the sampled
+        token (``logprobs=0`` -- the sampled token's logprob and rank -- is served), and logits
+        processors (sampling runs fused on the device)."""
+        from vllm import SamplingParams as VSamplingParams
+
+        if not isinstance(params, VSamplingParams):
+            raise ValueError("the B200 platform serves generation requests only (no pooling params)")
+        if getattr(params, "prompt_logprobs", None) is not None:
+            raise ValueError("prompt_logprobs are not supported by the B200 platform")
+        if params.logprobs is not None and params.logprobs > 0:
+            raise ValueError(f"logprobs={params.logprobs}: the B200 platform returns the sampled "
+                             "token's logprob only (logprobs=0)")
+        if getattr(params, "logits_processors", None):
+            raise ValueError("per-request logits processors are not supported by the B200 platform "
+                             "(sampling runs fused on the device)")
+
     # ---------------------------------------------------------------- configuration
     @classmethod
     def update_block_size_for_backend(cls, vllm_config) -> None:

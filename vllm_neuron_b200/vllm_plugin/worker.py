@@ -50,7 +50,7 @@ def convert_sampling_params(sp) -> SamplingParams:
     return SamplingParams(
         temperature=float(sp.temperature), top_k=int(top_k) if top_k > 0 else 0,
         top_p=float(sp.top_p) if sp.top_p is not None else 1.0, min_p=float(getattr(sp, "min_p", 0.0) or 0.0),
-        seed=sp.seed, max_tokens=sp.max_tokens, ignore_eos=True)
+        seed=sp.seed, max_tokens=sp.max_tokens, ignore_eos=True, logprobs=getattr(sp, "logprobs", None))
 
 
 class B200Worker(WorkerBase):
@@ -209,26 +209,46 @@ class B200Worker(WorkerBase):
             samples = start + n >= r.num_tokens
             out.scheduled.append(ScheduledRequest(r, start, n, samples))
         out.num_tokens = so.total_num_scheduled_tokens
-        toks, _ = self.runner.launch(out, False, self._bitmask(out, grammar_output)).result()
+        want_lp = any(sr.samples and sr.req.sampling_params.logprobs is not None for sr in out.scheduled)
+        handle = self.runner.launch(out, want_lp, self._bitmask(out, grammar_output), want_ranks=want_lp)
+        toks, lps = handle.result()
         req_ids, sampled = [], []
         row = 0
-        for sr in out.scheduled:
+        n = len(out.scheduled)
+        lp_ids = np.zeros((n, 1), dtype=np.int32) if want_lp else None
+        lp_val = np.zeros((n, 1), dtype=np.float32) if want_lp else None
+        lp_rank = np.zeros(n, dtype=np.int32) if want_lp else None
+        for i, sr in enumerate(out.scheduled):
             r = sr.req
             req_ids.append(r.request_id)
             r.num_computed_tokens = sr.start + sr.num_tokens
             if sr.samples:
                 t = int(toks[row])
+                if want_lp:
+                    lp_ids[i, 0] = t
+                    lp_val[i, 0] = float(lps[row])
+                    lp_rank[i] = int(handle.ranks[row])
                 row += 1
                 r.output_token_ids.append(t)
                 sampled.append([t])
             else:
                 sampled.append([])
+        logprobs = None
+        if want_lp:
+            from vllm.v1.outputs import LogprobsLists
+
+            logprobs = LogprobsLists(lp_ids, lp_val, lp_rank)
         return ModelRunnerOutput(req_ids=req_ids, req_id_to_index={rid: i for i, rid in enumerate(req_ids)},
-                                 sampled_token_ids=sampled, logprobs=None, prompt_logprobs_dict={},
+                                 sampled_token_ids=sampled, logprobs=logprobs, prompt_logprobs_dict={},
                                  pooler_output=[])
 
     def execute_dummy_batch(self) -> None:
-        return None
+        """An idle data-parallel replica's step: a one-token forward on the null block (no KV
+        written, nothing sampled) so that collectives spanning the replicas (the expert-parallel
+        exchange of wide-EP MoE layers) stay matched (reference: the DP dummy batch,
+        vllm/worker/neuron_model_runner.py:7710)."""
+        if self.runner is not None:
+            self.runner.dummy_forward()
 
     def take_draft_token_ids(self):
         return None

@@ -85,6 +85,7 @@ class ModelRunner:
         # keeps the dcp_rank-th slice of cache_block_size tokens (see set_dcp)
         self.dcp_size, self.dcp_rank, self.cache_block_size = 1, 0, block_size
         self.use_graphs = cuda_graphs and self.is_cuda and not envs.VLLM_B200_DISABLE_CUDA_GRAPHS
+        self._last_prefill_rows = ops.attention.PREFILL_ROWS  # rows per prefill work item
         cap = min(max_num_seqs, model.max_decode_tokens)
         self.graph_buckets = sorted(b for b in (graph_buckets or [1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128])
                                     if b <= cap)
@@ -106,6 +107,7 @@ class ModelRunner:
         self.dev_buf = torch.zeros(max_layout.total, dtype=torch.int32, device=self.device)
         self.tok_hosts = [torch.zeros(max_num_seqs, dtype=torch.int32, pin_memory=pin) for _ in range(2)]
         self.lp_hosts = [torch.zeros(max_num_seqs, dtype=torch.float32, pin_memory=pin) for _ in range(2)]
+        self.rank_hosts = [torch.zeros(max_num_seqs, dtype=torch.int32, pin_memory=pin) for _ in range(2)]
         self.tok_host, self.lp_host = self.tok_hosts[0], self.lp_hosts[0]
         # Device-resident last sampled token of every request slot (async decode inputs).
         self.max_slots = 2 * max_num_seqs + 8
@@ -113,6 +115,7 @@ class ModelRunner:
         self.last_tok = torch.zeros(self.max_slots, dtype=torch.int32, device=self.device)
         self.tok_dev = torch.zeros(max_num_seqs, dtype=torch.int32, device=self.device)
         self.lp_dev = torch.zeros(max_num_seqs, dtype=torch.float32, device=self.device)
+        self.rank_dev = torch.zeros(max_num_seqs, dtype=torch.int32, device=self.device)
         self.h2d_bytes = 0
         self.d2h_bytes = 0
         self.num_graph_replays = 0
@@ -296,8 +299,11 @@ class ModelRunner:
             h[o["nsplit"][0]] = min(real.num_splits, w.num_splits)
         else:
             kv_lens = (lsl if dcp > 1 else sl)[:Bp].astype(np.int64)
+            rows = ops.attention.prefill_rows(m.D, getattr(m, "kv_dtype", None), getattr(m, "block_size", 0),
+                                              G, dcp)
             w = ops.build_work(q_lens[:Bp], kv_lens, G, m.Hkv, self.num_sms,
-                               max_splits=m.attn_splits_max, head_dim=m.D)
+                               max_splits=m.attn_splits_max, head_dim=m.D, prefill_rows=rows)
+            self._last_prefill_rows = rows
             h[o["nsplit"][0]] = w.num_splits
         work = h[o["work"][0]:o["work"][0] + 2 * len(w.work)]
         work[:] = w.work.reshape(-1)
@@ -407,9 +413,11 @@ class ModelRunner:
         return fb, samp
 
     def _forward_and_sample(self, fb: ForwardBatch, samp: dict, S: int, tok_out: torch.Tensor,
-                            lp_out: torch.Tensor | None, bitmask: torch.Tensor | None = None):
+                            lp_out: torch.Tensor | None, bitmask: torch.Tensor | None = None,
+                            rank_out: torch.Tensor | None = None):
         tp = getattr(self.model, "tp", None)
-        if self.sampling_dp and bitmask is None and tp is not None and tp.world > 1 and tp.group is not None:
+        if (self.sampling_dp and bitmask is None and rank_out is None and tp is not None and tp.world > 1
+                and tp.group is not None):
             return self._sample_dp(fb, samp, S, tok_out, lp_out)
         logits = self.model.forward(fb)
         if bitmask is not None:
@@ -418,6 +426,14 @@ class ModelRunner:
                    samp["offsets"], min_p=samp["min_p"], out=tok_out[:S],
                    out_logprob=lp_out[:S] if lp_out is not None else None,
                    row_slots=samp["row_slots"], last_tok=self.last_tok)
+        if rank_out is not None:
+            # vLLM's logprob semantics: the sampled token's 1-based rank and its log-probability
+            # under the raw model distribution (before temperature / top-k / top-p)
+            lg = logits[:S].float()
+            sel = lg.gather(1, tok_out[:S].long()[:, None])
+            rank_out[:S].copy_((lg > sel).sum(1) + 1)
+            if lp_out is not None:
+                lp_out[:S].copy_((sel[:, 0] - torch.logsumexp(lg, dim=1)))
 
     def _sample_dp(self, fb: ForwardBatch, samp: dict, S: int, tok_out: torch.Tensor,
                    lp_out: torch.Tensor | None):
@@ -565,7 +581,7 @@ class ModelRunner:
 
     # ------------------------------------------------------------------ execute
     def launch(self, out: SchedulerOutput, want_logprobs: bool = False,
-               bitmask: torch.Tensor | None = None) -> "StepHandle":
+               bitmask: torch.Tensor | None = None, want_ranks: bool = False) -> "StepHandle":
         """Enqueue one step (inputs H2D, forward, sampling, tokens D2H) without waiting."""
         B = len(out.scheduled)
         if B == 0:
@@ -578,7 +594,7 @@ class ModelRunner:
         self.host_np = self.host_buf.numpy()
         tok_host, lp_host = self.tok_hosts[self._buf_idx], self.lp_hosts[self._buf_idx]
         bucket = None
-        if self.use_graphs and out.is_pure_decode and self.graphs and bitmask is None:
+        if self.use_graphs and out.is_pure_decode and self.graphs and bitmask is None and not want_ranks:
             for bb in sorted(self.graphs):
                 if bb >= B:
                     bucket = bb
@@ -607,11 +623,13 @@ class ModelRunner:
             self.h2d_bytes += n * 4
             fb, samp = self._views(dev, lay, B, S, W, decode, splits)
             fb.work = fb.work[:W]
+            fb.prefill_rows = self._last_prefill_rows
             self._attach_prompt_embeds(out, fb)
             self._begin_capture(out)
             if S > 0:
                 mask = bitmask.to(self.device, non_blocking=True) if bitmask is not None else None
-                self._forward_and_sample(fb, samp, S, self.tok_dev, self.lp_dev, mask)
+                self._forward_and_sample(fb, samp, S, self.tok_dev, self.lp_dev, mask,
+                                         self.rank_dev if want_ranks else None)
             else:
                 self.model.forward(fb)
             self.num_eager_steps += 1
@@ -625,11 +643,18 @@ class ModelRunner:
             lp_host[:S].copy_(lp_src[:S], non_blocking=self.is_cuda)
             self.d2h_bytes += S * 4
             lps = lp_host
+        ranks = None
+        if want_ranks:
+            ranks = self.rank_hosts[self._buf_idx]
+            ranks[:S].copy_(self.rank_dev[:S], non_blocking=self.is_cuda)
+            self.d2h_bytes += S * 4
         ev = None
         if self.is_cuda:
             ev = torch.cuda.Event()
             ev.record()
-        return StepHandle(ev, tok_host, lps, S)
+        h = StepHandle(ev, tok_host, lps, S)
+        h.rank_host = ranks
+        return h
 
     @torch.no_grad()
     def forward_logits(self, out: SchedulerOutput, hidden: bool = False) -> torch.Tensor:
@@ -647,6 +672,7 @@ class ModelRunner:
         dev.copy_(self.host_buf[:lay.total], non_blocking=self.is_cuda)
         fb, _ = self._views(dev, lay, B, S, W, decode, splits)
         fb.work = fb.work[:W]
+        fb.prefill_rows = self._last_prefill_rows
         self._attach_prompt_embeds(out, fb)
         fb.want_hidden = hidden
         self._begin_capture(out)
@@ -688,6 +714,12 @@ class StepHandle:
 
     def __init__(self, event, tok_host, lp_host, n: int):
         self.event, self.tok_host, self.lp_host, self.n = event, tok_host, lp_host, n
+        self.rank_host = None
+
+    @property
+    def ranks(self) -> np.ndarray | None:
+        """1-based ranks of the sampled tokens (launched with ``want_ranks``; after result())."""
+        return self.rank_host[:self.n].numpy().copy() if self.rank_host is not None else None
 
     def result(self) -> tuple[np.ndarray, np.ndarray | None]:
         if self.n == 0:
