@@ -120,15 +120,22 @@ void gemm_w8(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, int64_t 
              c10::optional<at::Tensor> gcount) {
   CHECK_CUDA(a);
   CHECK_CUDA(b);
-  TORCH_CHECK(w8 == 1 || w8 == 2, "gemm_w8: w8 must be 1 (A is the weight) or 2 (B)");
-  const at::Tensor& wt = w8 == 1 ? a : b;
-  const at::Tensor& act = w8 == 1 ? b : a;
-  TORCH_CHECK(wt.scalar_type() == at::kFloat8_e4m3fn, "gemm_w8: weight must be float8_e4m3fn");
+  TORCH_CHECK(w8 >= 1 && w8 <= 4, "gemm_w8: w8 must be 1 / 2 (block FP8 weight as A / B) or 3 / 4 (MXFP4)");
+  const bool fp4 = w8 >= 3;
+  const at::Tensor& wt = (w8 == 1 || w8 == 3) ? a : b;
+  const at::Tensor& act = (w8 == 1 || w8 == 3) ? b : a;
+  if (fp4) {
+    TORCH_CHECK(wt.scalar_type() == at::kByte, "gemm_w8: MXFP4 weight must be uint8 (packed e2m1)");
+    TORCH_CHECK(scales.scalar_type() == at::kByte && scales.stride(-1) == 1,
+                "gemm_w8: MXFP4 scales must be uint8 e8m0 [rows, K / 32]");
+  } else {
+    TORCH_CHECK(wt.scalar_type() == at::kFloat8_e4m3fn, "gemm_w8: weight must be float8_e4m3fn");
+    TORCH_CHECK(scales.scalar_type() == at::kFloat && scales.dim() == 2 && scales.stride(1) == 1,
+                "gemm_w8: scales must be fp32 [row blocks, k blocks]");
+  }
   CHECK_BF16(act);
-  TORCH_CHECK(scales.scalar_type() == at::kFloat && scales.dim() == 2 && scales.stride(1) == 1,
-              "gemm_w8: scales must be fp32 [row blocks, k blocks]");
   const bool grouped = gtiles.has_value();
-  TORCH_CHECK(!grouped || w8 == 2, "gemm_w8: grouped mode takes the weight as B");
+  TORCH_CHECK(!grouped || w8 == 2 || w8 == 4, "gemm_w8: grouped mode takes the weight as B");
   TORCH_CHECK(a.stride(-1) == 1 && b.stride(-1) == 1 && out.stride(-1) == 1,
               "gemm_w8: inner dims must be contiguous");
   const bool f32_out = (epi == b200::EPI_F32_RED || epi == b200::EPI_F32_RED_T);
@@ -142,17 +149,18 @@ void gemm_w8(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, int64_t 
   g.ldb = b.stride(-2);
   g.ldo = out.stride(0);
   g.M = (int)a.size(0);
-  g.K = (int)a.size(-1);
+  g.K = (int)act.size(-1);  // logical elements (an MXFP4 row holds K / 2 bytes)
+  TORCH_CHECK(wt.size(-1) * (fp4 ? 2 : 1) == g.K, "gemm_w8: weight and activation K differ");
   if (grouped) {
-    TORCH_CHECK(b.dim() == 3 && b.is_contiguous() && b.size(2) == a.size(1), "gemm_w8: grouped b");
-    TORCH_CHECK(b.size(1) % 128 == 0, "gemm_w8: grouped expert rows must be multiples of 128");
+    TORCH_CHECK(b.dim() == 3 && b.is_contiguous(), "gemm_w8: grouped b");
+    TORCH_CHECK(fp4 || b.size(1) % 128 == 0, "gemm_w8: grouped block-FP8 expert rows must be multiples of 128");
     g.N = (int)b.size(1);
     g.gtiles = gtiles->data_ptr<int>();
     g.gcount = gcount.value().data_ptr<int>();
     g.gmax = (int)gtiles->size(0);
     g.num_groups = (int)b.size(0);
   } else {
-    TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.size(1) == b.size(1), "gemm_w8: bad shapes");
+    TORCH_CHECK(a.dim() == 2 && b.dim() == 2, "gemm_w8: bad shapes");
     g.N = (int)b.size(0);
   }
   g.bn = (int)bn;
@@ -160,9 +168,16 @@ void gemm_w8(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, int64_t 
   g.splits = (int)splits;
   g.status = status_word();
   g.w8 = (int)w8;
-  g.w_scales = scales.data_ptr<float>();
-  g.w_scale_ld = (int)scales.stride(0);
-  g.w_scale_rows = (int)scales.size(0);
+  if (fp4) {
+    g.w_scales8 = scales.data_ptr<uint8_t>();
+    g.w_scale_ld = (int)scales.size(-1);
+    g.w_scale_rows = (int)(scales.numel() / scales.size(-1));
+    TORCH_CHECK(scales.is_contiguous(), "gemm_w8: MXFP4 scales must be contiguous");
+  } else {
+    g.w_scales = scales.data_ptr<float>();
+    g.w_scale_ld = (int)scales.stride(0);
+    g.w_scale_rows = (int)scales.size(0);
+  }
   if (g.M == 0 || g.N == 0) return;
   b200::gemm_bf16_launch(g, cur_stream());
   check_launch("gemm_w8");

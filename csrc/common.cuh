@@ -128,7 +128,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
 // raised `*abort`, so that a CTA whose pipeline stalled reaches its teardown quickly.
 __device__ __forceinline__ bool mbar_wait_abortable(uint64_t* bar, uint32_t parity,
                                                     uint32_t code, uint32_t* status,
-                                                    volatile int* abort) {
+                                                    volatile int* abort,
+                                                    uint64_t timeout_ns = B200_WAIT_TIMEOUT_NS) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   uint32_t n = 0;
@@ -136,7 +137,7 @@ __device__ __forceinline__ bool mbar_wait_abortable(uint64_t* bar, uint32_t pari
     if (mbar_try_wait(bar, parity)) return true;
     if ((++n & 63u) == 0) {
       if (*abort) return false;
-      if (globaltimer_ns() - t0 > B200_WAIT_TIMEOUT_NS) {
+      if (globaltimer_ns() - t0 > timeout_ns) {
         set_status(status, code);
         *abort = 1;
         return false;

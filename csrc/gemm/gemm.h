@@ -65,6 +65,10 @@ struct GemmArgs {
   const float* w_scales = nullptr;
   int w_scale_ld = 0;
   int w_scale_rows = 0;
+  // MXFP4 weight (w8 = 3 when A, 4 when B is the weight): e2m1 nibbles packed two per byte
+  // (lower k in the low nibble), rows of K / 2 bytes (lda / ldb in bytes), with one e8m0 scale
+  // byte per 32 elements: w_scales8 [w_scale_rows][w_scale_ld] (one row per weight row).
+  const uint8_t* w_scales8 = nullptr;
 };
 
 void gemm_bf16_launch(const GemmArgs& args, cudaStream_t stream);

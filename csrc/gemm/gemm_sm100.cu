@@ -75,6 +75,7 @@ struct GemmParams {
   // 128 x 128 block of the weight
   const float* wsc;
   int wsc_ld, wsc_rows;
+  const uint8_t* wsc8;  // MXFP4: e8m0 scale bytes [wsc_rows][wsc_ld], one per 32 elements
 };
 
 // Bounded wait until a monotonic counter (written by a peer with a system-scope release)
@@ -187,6 +188,19 @@ struct TmemCols {
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
 
+// Four bytes of e2m1 pairs -> four f16x2 (the low nibble of each byte in the low half); every
+// e2m1 value is exact in f16.
+__device__ __forceinline__ void fp4x8_to_f16x8_gemm(uint32_t w, uint32_t (&o)[4]) {
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+      : "=r"(o[0]), "=r"(o[1]), "=r"(o[2]), "=r"(o[3])
+      : "r"(w));
+}
+
 // FP8 = true: e4m3 operands (kind::f8f6f4).  A 128-byte swizzle row then holds 128 elements, so
 // the shared-memory tiles and the per-instruction descriptor advance (32 bytes) are unchanged;
 // only the k-block element count, the MMA kind and the epilogue scale differ.
@@ -197,18 +211,24 @@ __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)
 // tile's block scale, bf16(e4m3 * scale), into the 128-byte-swizzled bf16 operand layout the
 // MMA descriptors read, and release the stage to the MMA issuer (conv_bar).  Weight bytes cross
 // HBM once at one byte per element; the tensor cores run kind::f16.
+// W8 = 3 / 4: the same for an MXFP4 weight on A / B (GPT-OSS experts): 32 packed bytes per row
+// per stage (two e2m1 per byte), widened with the hardware e2m1x2 conversion and the e8m0
+// scale of each 32-element block -- half a byte per element from HBM.
 template <int BN, int STAGES, int EPI, bool FP8 = false, int W8 = 0>
 __global__ void __launch_bounds__(W8 ? 320 : 192, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA,
                      const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
   constexpr int kBTileBytes = BN * kBK * 2;
-  constexpr int kW8Rows = W8 == 1 ? kBM : W8 == 2 ? BN : 0;  // weight rows per tile
-  constexpr int kSBytes = kW8Rows * kBK;                      // fp8 staging bytes per stage
+  constexpr bool kFP4 = W8 >= 3;                             // MXFP4 (else block FP8)
+  constexpr int kWSide = W8 == 0 ? 0 : (W8 == 1 || W8 == 3) ? 1 : 2;  // weight operand: A / B
+  constexpr int kW8Rows = kWSide == 1 ? kBM : kWSide == 2 ? BN : 0;  // weight rows per tile
+  constexpr int kSRow = kFP4 ? kBK / 2 : kBK;                 // staged bytes per row per stage
+  constexpr int kSBytes = kW8Rows * kSRow;                    // staging bytes per stage
   constexpr int kStageBytes = kATileBytes + kBTileBytes + kSBytes;
   // bytes the TMA delivers per stage (the converted operand is written by the converter)
-  constexpr int kStageTx = W8 == 1   ? kSBytes + kBTileBytes
-                           : W8 == 2 ? kATileBytes + kSBytes
-                                     : kATileBytes + kBTileBytes;
+  constexpr int kStageTx = kWSide == 1   ? kSBytes + kBTileBytes
+                           : kWSide == 2 ? kATileBytes + kSBytes
+                                         : kATileBytes + kBTileBytes;
   constexpr uint32_t kTmemCols = TmemCols<BN>::v;
   constexpr uint32_t kIdesc = make_idesc_f16(kBM, BN, !FP8);  // FP8: type fields 0 = E4M3
   constexpr int kKElems = FP8 ? 2 * kBK : kBK;                  // elements per k-block
@@ -231,6 +251,9 @@ __global__ void __launch_bounds__(W8 ? 320 : 192, 1)
 
   const int warp = warp_id();
   const int lane = lane_id();
+  // a GEMM whose producer waits for peers' all-gathered rows stalls with them: its pipeline
+  // waits get the cross-rank budget
+  const uint64_t wait_ns = p.sp.ag_ctr != nullptr ? B200_PEER_TIMEOUT_NS : B200_WAIT_TIMEOUT_NS;
 
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmA);
@@ -281,13 +304,14 @@ __global__ void __launch_bounds__(W8 ? 320 : 192, 1)
           // peer stores (generic proxy) -> this thread's TMA reads (async proxy)
           if (waited) asm volatile("fence.proxy.async.global;" ::: "memory");
         }
-        uint8_t* dst = W8 == 1 ? smS + s * kSBytes : smA + s * kATileBytes;
-        tma_load_2d(&tmA, &full_bar[s], dst, kb * kKElems, a_row, hint_a);
+        uint8_t* dst = kWSide == 1 ? smS + s * kSBytes : smA + s * kATileBytes;
+        tma_load_2d(&tmA, &full_bar[s], dst, (kFP4 && kWSide == 1) ? kb * kSRow : kb * kKElems, a_row, hint_a);
       };
       auto load_b = [&](int s, int kb, int nb, int mb) {
         const int base = p.grouped ? tile_rows(p, mb).b_base : 0;
-        uint8_t* dst = W8 == 2 ? smS + s * kSBytes : smB + s * kBTileBytes;
-        tma_load_2d(&tmB, &full_bar[s], dst, kb * kKElems, base + nb * BN, hint_b);
+        uint8_t* dst = kWSide == 2 ? smS + s * kSBytes : smB + s * kBTileBytes;
+        tma_load_2d(&tmB, &full_bar[s], dst, (kFP4 && kWSide == 2) ? kb * kSRow : kb * kKElems,
+                    base + nb * BN, hint_b);
       };
       // The grouped tile list is written by the previous kernel.
       if (p.grouped) pdl_wait();
@@ -328,7 +352,7 @@ __global__ void __launch_bounds__(W8 ? 320 : 192, 1)
       while (have) {
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
-        if (!mbar_wait_abortable(&empty_bar[s], ph ^ 1, kTimeoutSmemEmpty, p.status, abort_flag)) {
+        if (!mbar_wait_abortable(&empty_bar[s], ph ^ 1, kTimeoutSmemEmpty, p.status, abort_flag, wait_ns)) {
           ok = false;
           break;
         }
@@ -362,7 +386,7 @@ __global__ void __launch_bounds__(W8 ? 320 : 192, 1)
       for (; ok && cur.next(p, mb, nb, k0, k1); ++t_local) {
         const int acc = t_local & 1;
         const uint32_t aph = (t_local >> 1) & 1;
-        if (!mbar_wait_abortable(&tempty_bar[acc], aph ^ 1, kTimeoutTmemEmpty, p.status, abort_flag)) {
+        if (!mbar_wait_abortable(&tempty_bar[acc], aph ^ 1, kTimeoutTmemEmpty, p.status, abort_flag, wait_ns)) {
           ok = false;
           break;
         }
@@ -372,7 +396,7 @@ __global__ void __launch_bounds__(W8 ? 320 : 192, 1)
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait_abortable(W8 ? &conv_bar[s] : &full_bar[s], ph, kTimeoutTmaFull, p.status,
-                                   abort_flag)) {
+                                   abort_flag, wait_ns)) {
             ok = false;
             break;
           }
@@ -407,16 +431,50 @@ __global__ void __launch_bounds__(W8 ? 320 : 192, 1)
     int mb, nb, k0, k1;
     while (ok && cur.next(p, mb, nb, k0, k1)) {
       const TileRows tr = tile_rows(p, mb);
-      const int wrow0 = W8 == 1 ? tr.a_row : tr.b_base + nb * BN;  // first weight row of the tile
+      const int wrow0 = kWSide == 1 ? tr.a_row : tr.b_base + nb * BN;  // first weight row of the tile
       for (int kb = k0; kb < k1; ++kb, ++it) {
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
-        if (!mbar_wait_abortable(&full_bar[s], ph, kTimeoutTmaFull, p.status, abort_flag)) {
+        if (!mbar_wait_abortable(&full_bar[s], ph, kTimeoutTmaFull, p.status, abort_flag, wait_ns)) {
           ok = false;
           break;
         }
         const uint8_t* src = smS + s * kSBytes;
-        uint8_t* dst = W8 == 1 ? smA + s * kATileBytes : smB + s * kBTileBytes;
+        uint8_t* dst = kWSide == 1 ? smA + s * kATileBytes : smB + s * kBTileBytes;
+        if constexpr (kFP4) {
+          // lane: row r, 8 packed bytes = elements [16 c, 16 c + 16) of this 64-k block, whose
+          // e8m0 scale is block kb * 2 + c / 2 of the row
+#pragma unroll
+          for (int i = 0; i < kW8Rows / 32; ++i) {
+            const int r = cw * (kW8Rows / 4) + i * 8 + (lane >> 2);
+            const int c = lane & 3;
+            const uint2 v = *reinterpret_cast<const uint2*>(src + r * kSRow + c * 8);
+            const int wr = min(wrow0 + r, p.wsc_rows - 1);
+            const uint32_t e = __ldg(p.wsc8 + (long long)wr * p.wsc_ld + kb * 2 + (c >> 1));
+            const float sc = __uint_as_float(e ? (e << 23) : 0x00400000u);  // 2^(e - 127)
+            uint32_t h[8];
+            {
+              uint32_t t0[4], t1[4];
+              fp4x8_to_f16x8_gemm(v.x, t0);
+              fp4x8_to_f16x8_gemm(v.y, t1);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                h[j] = t0[j];
+                h[4 + j] = t1[j];
+              }
+            }
+            uint32_t o[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h[j]));
+              o[j] = pack_bf16x2(f.x * sc, f.y * sc);
+            }
+            uint8_t* drow = dst + r * 128;
+            const int sw = r & 7;
+            *reinterpret_cast<uint4*>(drow + (((2 * c) ^ sw) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+            *reinterpret_cast<uint4*>(drow + (((2 * c + 1) ^ sw) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
+          }
+        } else {
         const float* sc_col = p.wsc + (kb >> 1);  // 128-wide scale column of this 64-k block
 #pragma unroll
         for (int i = 0; i < kW8Rows / 32; ++i) {
@@ -440,6 +498,7 @@ __global__ void __launch_bounds__(W8 ? 320 : 192, 1)
           *reinterpret_cast<uint4*>(drow + (((2 * c16) ^ sw) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
           *reinterpret_cast<uint4*>(drow + (((2 * c16 + 1) ^ sw) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
         }
+        }
         // generic-proxy shared-memory writes -> the tensor cores' (async proxy) operand reads
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
@@ -457,7 +516,7 @@ __global__ void __launch_bounds__(W8 ? 320 : 192, 1)
     for (; cur.next(p, mb, nb, k0, k1); ++t_local) {
       const int acc = t_local & 1;
       const uint32_t aph = (t_local >> 1) & 1;
-      if (!mbar_wait_abortable(&tfull_bar[acc], aph, kTimeoutTmemFull, p.status, abort_flag)) break;
+      if (!mbar_wait_abortable(&tfull_bar[acc], aph, kTimeoutTmemFull, p.status, abort_flag, wait_ns)) break;
       tc_fence_after();
       const TileRows trows = tile_rows(p, mb);
       const int m = trows.a_row + row;
@@ -661,8 +720,9 @@ CUtensorMap make_tmap_u8_2d(const void* ptr, uint64_t inner, uint64_t outer, uin
 template <int BN, int STAGES, int EPI, bool FP8 = false, int W8 = 0>
 static void launch_impl(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
                         int grid, cudaStream_t stream) {
-  constexpr int w8_rows = W8 == 1 ? kBM : W8 == 2 ? BN : 0;
-  constexpr int smem = STAGES * (kATileBytes + BN * kBK * 2 + w8_rows * kBK) + 1024 + 256;
+  constexpr int w8_rows = (W8 == 1 || W8 == 3) ? kBM : (W8 == 2 || W8 == 4) ? BN : 0;
+  constexpr int srow = W8 >= 3 ? kBK / 2 : kBK;
+  constexpr int smem = STAGES * (kATileBytes + BN * kBK * 2 + w8_rows * srow) + 1024 + 256;
   static_assert(smem <= 232448, "shared memory budget");
   auto kern = gemm_bf16_kernel<BN, STAGES, EPI, FP8, W8>;
   static std::atomic<uint64_t> configured{0};  // per instantiation, per device
@@ -693,21 +753,33 @@ void gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
   if (a.fp8 && (grouped || a.sp != nullptr))
     throw std::invalid_argument("gemm: FP8 operands are for the dense (non-grouped, non-SP) modes");
   const uint64_t b_rows = grouped ? (uint64_t)a.N * a.num_groups : (uint64_t)a.N;
-  if (a.w8 != 0) {
-    if (a.fp8 || (a.w8 != 1 && a.w8 != 2) || a.w_scales == nullptr || a.w_scale_rows < 1 ||
-        a.w_scale_ld < (a.K + 127) / 128)
+  const bool w4 = a.w8 == 3 || a.w8 == 4;
+  if (a.w8 == 1 || a.w8 == 2) {
+    if (a.fp8 || a.w_scales == nullptr || a.w_scale_rows < 1 || a.w_scale_ld < (a.K + 127) / 128)
       throw std::invalid_argument("gemm: bad block-FP8 weight arguments");
     if (a.K % 16 != 0 || (a.w8 == 1 ? a.lda : a.ldb) % 16 != 0)
       throw std::invalid_argument("gemm: block-FP8 weight rows must be multiples of 16 bytes");
     const uint64_t wrows = a.w8 == 1 ? (uint64_t)a.M : b_rows;
     if ((uint64_t)a.w_scale_rows < (wrows + 127) / 128)
       throw std::invalid_argument("gemm: block-FP8 scale rows do not cover the weight rows");
+  } else if (w4) {
+    if (a.fp8 || a.w_scales8 == nullptr || a.K % 64 != 0 || a.w_scale_ld < a.K / 32)
+      throw std::invalid_argument("gemm: bad MXFP4 weight arguments (K must be a multiple of 64)");
+    if ((a.w8 == 3 ? a.lda : a.ldb) % 16 != 0)
+      throw std::invalid_argument("gemm: MXFP4 weight rows must be multiples of 16 bytes");
+    const uint64_t wrows = a.w8 == 3 ? (uint64_t)a.M : b_rows;
+    if ((uint64_t)a.w_scale_rows < wrows)
+      throw std::invalid_argument("gemm: MXFP4 scale rows do not cover the weight rows");
+  } else if (a.w8 != 0) {
+    throw std::invalid_argument("gemm: w8 must be 0..4");
   }
   // block-FP8 weight operand: bytes, 64 per row per stage, no swizzle (the converter swizzles)
-  const CUtensorMap ta = a.w8 == 1 ? make_tmap_u8_2d(a.A, a.K, a.M, a.lda, kBK, kBM, 0)
+  const CUtensorMap ta = a.w8 == 3 ? make_tmap_u8_2d(a.A, a.K / 2, a.M, a.lda, kBK / 2, kBM, 0)
+                         : a.w8 == 1 ? make_tmap_u8_2d(a.A, a.K, a.M, a.lda, kBK, kBM, 0)
                          : a.fp8   ? make_tmap_u8_2d(a.A, a.K, a.M, a.lda, 128, kBM, 128)
                                    : make_tmap_bf16_2d(a.A, a.K, a.M, a.lda, kBK, kBM, true);
-  const CUtensorMap tb = a.w8 == 2 ? make_tmap_u8_2d(a.B, a.K, b_rows, a.ldb, kBK, bn, 0)
+  const CUtensorMap tb = a.w8 == 4 ? make_tmap_u8_2d(a.B, a.K / 2, b_rows, a.ldb, kBK / 2, bn, 0)
+                         : a.w8 == 2 ? make_tmap_u8_2d(a.B, a.K, b_rows, a.ldb, kBK, bn, 0)
                          : a.fp8   ? make_tmap_u8_2d(a.B, a.K, b_rows, a.ldb, 128, bn, 128)
                                    : make_tmap_bf16_2d(a.B, a.K, b_rows, a.ldb, kBK, bn, true);
   GemmParams p;
@@ -725,6 +797,7 @@ void gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
   p.wsc = a.w_scales;
   p.wsc_ld = a.w_scale_ld;
   p.wsc_rows = a.w_scale_rows;
+  p.wsc8 = a.w_scales8;
   p.streamk = a.splits < 0 ? 1 : 0;
   int splits = a.splits < 1 ? 1 : a.splits;
   if (splits > p.num_k_blocks) splits = p.num_k_blocks;
@@ -798,7 +871,14 @@ void gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
     B200_GEMM_W8_CASE(2, 128, 5, EPI_F32_RED)
     B200_GEMM_W8_CASE(2, 256, 3, EPI_BF16_RS)
     B200_GEMM_W8_CASE(2, 128, 5, EPI_BF16_RS)
-    throw std::invalid_argument("gemm (block fp8): unsupported (operand, bn, epilogue): w8=" +
+    // MXFP4 weights
+    B200_GEMM_W8_CASE(3, 16, 8, EPI_F32_RED_T)
+    B200_GEMM_W8_CASE(3, 32, 8, EPI_F32_RED_T)
+    B200_GEMM_W8_CASE(3, 64, 7, EPI_F32_RED_T)
+    B200_GEMM_W8_CASE(3, 128, 5, EPI_F32_RED_T)
+    B200_GEMM_W8_CASE(4, 256, 3, EPI_BF16)
+    B200_GEMM_W8_CASE(4, 128, 5, EPI_BF16)
+    throw std::invalid_argument("gemm (fp8 / fp4 weight): unsupported (operand, bn, epilogue): w8=" +
                                 std::to_string(a.w8) + " bn=" + std::to_string(bn) +
                                 " epi=" + std::to_string(a.epi));
   }

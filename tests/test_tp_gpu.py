@@ -37,7 +37,7 @@ torch.cuda.set_device(int(os.environ["LOCAL_RANK"]))
 llm = LLM(ckpt, tensor_parallel_size=int(os.environ["WORLD_SIZE"]), max_num_seqs=8, max_model_len=256,
           num_gpu_blocks=256, max_num_batched_tokens=256, skip_tokenizer_init=True,
           additional_config={"b200_config": {"fused_comm": fused, "sequence_parallel": sp,
-                                             "sampling_dp": sdp}})
+                                             "fused_sp": fused and sp, "sampling_dp": sdp}})
 g = torch.Generator().manual_seed(0)
 prompts = [torch.randint(0, 32000, (40,), generator=g).tolist() for _ in range(6)]
 lg_long = llm.engine.prompt_logits(prompts)

@@ -189,6 +189,7 @@ class B200Config:
     sequence_parallel: bool = False   # prefill: reduce-scatter / all-gather instead of all-reduce
     cuda_graphs: bool = True
     fused_comm: bool = True           # fused GEMM+collective kernels (else NCCL baseline)
+    fused_sp: bool = False            # sequence-parallel prefill on the fused RS/AG GEMMs (else NCCL)
     use_cublas_baseline: bool = False  # library GEMMs instead of the tcgen05 kernels
     sampling_dp: bool = False          # TP decode: each rank samples 1/W of the rows (all-to-all)
     vision_tp_size: int = 1            # vision encoder sharded over this many consecutive TP ranks

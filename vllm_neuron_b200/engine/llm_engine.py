@@ -143,7 +143,7 @@ def build_model(args: EngineArgs, tp: GroupComm = SINGLE):
             and not envs.VLLM_B200_DISABLE_FUSED_COMM):
         from ..parallel import state as ps
 
-        model.enable_fused_comm(ps.get_parallel_state().cpu)
+        model.enable_fused_comm(ps.get_parallel_state().cpu, fused_sp=b200_config.fused_sp)
     return arch, model, model_path, device, b200_config
 
 

@@ -19,6 +19,7 @@ from __future__ import annotations
 import torch
 
 from .. import envs, ops
+from ..ops import linear as L
 from ..ops import moe as M
 from .llama import LlamaForCausalLM
 from .qwen_moe import MoEMixin
@@ -109,17 +110,30 @@ class GptOssForCausalLM(MoEMixin, LlamaForCausalLM):
     @torch.no_grad()
     def set_expert_mxfp4(self, ly, gu_blocks=None, gu_scales=None, dn_blocks=None, dn_scales=None):
         """Install the layer's MXFP4 experts: from checkpoint blocks/scales (gate/up rows in
-        this model's gate-then-up order), or by quantizing the current bf16 weights; the bf16
-        copies are set to the dequantized values so prefill and decode use the same weights."""
+        this model's gate-then-up order), or by quantizing the current bf16 weights.  The expert
+        stacks become :class:`~..ops.linear.MXFP4Weight` (the bf16 copies are dropped): every
+        batch runs them W4A16 on the tcgen05 grouped GEMM, and decode batches of at most
+        ``VLLM_B200_FP4_DECODE_MAX_TOKENS`` tokens may use the fp4 mma.sync kernel on its own
+        packed tiles instead (0 disables it)."""
         if not self.use_fp4:
             return
         if gu_blocks is None:
+            if isinstance(ly.w_gu, L.MXFP4Weight):
+                return
             gu_blocks, gu_scales = _quant_experts(ly.w_gu)
             dn_blocks, dn_scales = _quant_experts(ly.w_down)
-        ly.w_gu.copy_(dequant_mxfp4(gu_blocks, gu_scales).to(ly.w_gu.device))
-        ly.w_down.copy_(dequant_mxfp4(dn_blocks, dn_scales).to(ly.w_down.device))
-        ly.fp4_gu = M.pack_mxfp4(gu_blocks.to(self.device), gu_scales.to(self.device))
-        ly.fp4_down = M.pack_mxfp4(dn_blocks.to(self.device), dn_scales.to(self.device))
+        dev = self.device
+        gu = L.MXFP4Weight.from_blocks(gu_blocks.to(dev), gu_scales.to(dev))
+        dn = L.MXFP4Weight.from_blocks(dn_blocks.to(dev), dn_scales.to(dev))
+        if self.fp4_max_tokens > 0:
+            ly.fp4_gu = M.pack_mxfp4(gu_blocks.to(dev), gu_scales.to(dev))
+            ly.fp4_down = M.pack_mxfp4(dn_blocks.to(dev), dn_scales.to(dev))
+        for name, w in (("w_gu", gu), ("w_down", dn)):
+            if name in ly._parameters:
+                del ly._parameters[name]
+            setattr(ly, name, w)
+        if dev.type == "cuda":
+            torch.cuda.empty_cache()
 
     def _mlp(self, i, ly, x, res, nxt_norm, T, small, fused):
         h = self.ws_h[:T]

@@ -199,15 +199,17 @@ class LlamaForCausalLM(torch.nn.Module):
             else:
                 prm.normal_(0.0, std, generator=g)
 
-    def enable_fused_comm(self, cpu_group=None):
-        """Use the fused one-shot all-reduce + residual + RMSNorm kernel for TP decode."""
+    def enable_fused_comm(self, cpu_group=None, fused_sp: bool = True):
+        """Use the fused one-shot all-reduce + residual + RMSNorm kernel for TP decode, and with
+        ``fused_sp`` (and sequence parallelism on) the fused reduce-scatter / all-gather GEMMs for
+        prefill."""
         if self.tp.world > 1 and self.device.type == "cuda":
             from ..parallel.fused import TPFusedComm
 
             self.tp_fused = TPFusedComm(self.tp, self.H, self.max_decode_tokens, self.device, cpu_group)
             # Sequence-parallel prefill with the all-gather / reduce-scatter fused into the GEMMs
             # and the norm: dense SwiGLU decoders without an o_proj bias
-            if (self.sequence_parallel and type(self)._mlp is LlamaForCausalLM._mlp
+            if (fused_sp and self.sequence_parallel and type(self)._mlp is LlamaForCausalLM._mlp
                     and all(getattr(ly, "o_bias", None) is None for ly in self.layers)
                     and (not getattr(self, "fp8_linears", 0) or getattr(self, "block_fp8", False))):
                 from ..parallel.fused import SPFusedComm

@@ -64,7 +64,7 @@ class SyntheticForCausalLM(torch.nn.Module):
     def load_hf_state_dict(self, get_tensor, names):
         pass
 
-    def enable_fused_comm(self, cpu_group=None):
+    def enable_fused_comm(self, cpu_group=None, fused_sp: bool = False):
         pass
 
     def _expected(self, pos: torch.Tensor, layer: int) -> torch.Tensor:

@@ -119,6 +119,49 @@ class BlockFP8Weight:
         return self.dequant(torch.float32).to(torch.bfloat16)
 
 
+# e2m1 code points (sign bit 3, exponent bits 2-1, mantissa bit 0)
+FP4_VALUES = [0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0, -0.0, -0.5, -1.0, -1.5, -2.0, -3.0, -4.0, -6.0]
+
+
+class MXFP4Weight:
+    """MXFP4 weight ``[N, K]`` or expert stack ``[E, N, K]`` in the OCP MX layout of GPT-OSS
+    checkpoints: ``q [..., N, K / 2]`` uint8 (two e2m1 values per byte, the lower k in the low
+    nibble) and ``scales [..., N, K / 32]`` uint8 (e8m0, value ``2 ** (s - 127)``).  Served W4A16 on
+    the tcgen05 GEMM: the packed bytes stream from HBM at half a byte per element and each tile is
+    widened in shared memory (``e2m1 * scale`` is exact in bf16); bf16 activations, fp32
+    accumulation.  K must be a multiple of 64."""
+
+    def __init__(self, q: torch.Tensor, scales: torch.Tensor):
+        assert q.dtype == torch.uint8 and scales.dtype == torch.uint8
+        assert q.shape[:-1] == scales.shape[:-1] and scales.shape[-1] * 16 == q.shape[-1]
+        self.q = q.contiguous()
+        self.scales = scales.contiguous()
+
+    @classmethod
+    def from_blocks(cls, blocks: torch.Tensor, scales: torch.Tensor) -> "MXFP4Weight":
+        """Checkpoint tensors ``blocks [..., K / 32, 16]`` and ``scales [..., K / 32]``."""
+        return cls(blocks.reshape(*blocks.shape[:-2], blocks.shape[-2] * 16), scales)
+
+    @property
+    def shape(self):
+        return (*self.q.shape[:-1], self.q.shape[-1] * 2)
+
+    @property
+    def device(self):
+        return self.q.device
+
+    def dequant(self, dtype=torch.float32) -> torch.Tensor:
+        lut = torch.tensor(FP4_VALUES, dtype=torch.float32, device=self.q.device)
+        b = self.q.to(torch.int64)
+        v = torch.stack([lut[b & 0x0F], lut[b >> 4]], dim=-1).reshape(*self.q.shape[:-1], -1)
+        e = self.scales.to(torch.float32) - 127.0
+        v = v.reshape(*v.shape[:-1], -1, 32) * torch.pow(2.0, e)[..., None]
+        return v.reshape(self.shape).to(dtype)
+
+    def dequant_bf16_ref(self) -> torch.Tensor:
+        return self.dequant(torch.float32).to(torch.bfloat16)
+
+
 def quantize_fp8(x: torch.Tensor, scale: float, out: torch.Tensor | None = None) -> torch.Tensor:
     """``satfinite(x / scale)`` as ``torch.float8_e4m3fn`` (the rule of the quant kernels)."""
     if out is None:

@@ -116,8 +116,8 @@ def route_ref(logits: torch.Tensor, k: int, mode: int, renorm: bool = True,
 
 
 def _dense(w):
-    """bf16 tensor view of a weight (block-FP8 weights: the bf16 operand the kernels use)."""
-    return w.dequant_bf16_ref() if isinstance(w, L.BlockFP8Weight) else w
+    """bf16 tensor view of a weight (block-FP8 / MXFP4 weights: the bf16 operand the kernels use)."""
+    return w.dequant_bf16_ref() if isinstance(w, (L.BlockFP8Weight, L.MXFP4Weight)) else w
 
 
 def experts_ref(x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, w_gu: torch.Tensor,
@@ -323,6 +323,8 @@ def _experts_cuda(x, ids, w, w_gu, w_down, k, b_gu, b_down, act, alpha, limit, e
         ext().moe_mxfp4_gemm(xp, fp4_gu, gu, gt, ws.gcount)
     elif isinstance(w_gu, L.BlockFP8Weight):
         ext().gemm_w8(xp, w_gu.q, gu, EPI_BF16, 256, 1, w_gu.scales, 2, ws.gtiles, ws.gcount)
+    elif isinstance(w_gu, L.MXFP4Weight):
+        ext().gemm_w8(xp, w_gu.q, gu, EPI_BF16, 256, 1, w_gu.scales, 4, ws.gtiles, ws.gcount)
     else:
         ext().gemm_grouped(xp, w_gu, gu, ws.gtiles, ws.gcount, EPI_BF16, 256)
     a = ws.act[:R, :I]
@@ -333,6 +335,8 @@ def _experts_cuda(x, ids, w, w_gu, w_down, k, b_gu, b_down, act, alpha, limit, e
         ext().moe_mxfp4_gemm(a, fp4_down, y, gt, ws.gcount)
     elif isinstance(w_down, L.BlockFP8Weight):
         ext().gemm_w8(a, w_down.q, y, EPI_BF16, bn_down, 1, w_down.scales, 2, ws.gtiles, ws.gcount)
+    elif isinstance(w_down, L.MXFP4Weight):
+        ext().gemm_w8(a, w_down.q, y, EPI_BF16, bn_down, 1, w_down.scales, 4, ws.gtiles, ws.gcount)
     else:
         ext().gemm_grouped(a, w_down, y, ws.gtiles, ws.gcount, EPI_BF16, bn_down)
     ext().moe_combine(y, ws.inv_pos[:R], w, ids, b_down, e_start, shared, shared_gate, out)

@@ -123,13 +123,14 @@ class ModelRunner:
         self.graph_kernels: dict[int, int] = {}  # kernels recorded per captured bucket
         self.replayed_kernels = 0
         self.kv_cache = None
-        # Snapshot capture: when set, the packed inputs of every step are saved to this
-        # directory (reference: vllm_neuron/snapshot/*, runtime input capture).
-        import os
+        # Snapshot capture of selected steps' packed inputs (snapshot/: VLLM_B200_SNAPSHOT_*;
+        # reference: vllm_neuron/snapshot/*, runtime input capture).
+        from ..snapshot import SnapshotCapturer, SnapshotConfig
 
-        self.snapshot_dir = envs.VLLM_B200_SNAPSHOT_DIR
-        self.snapshot_max = envs.VLLM_B200_SNAPSHOT_MAX_STEPS
-        self._snap_n = 0
+        tp = getattr(model, "tp", None)
+        self.snapshot = SnapshotCapturer(SnapshotConfig.from_env(), rank=getattr(tp, "rank", 0),
+                                         world=getattr(tp, "world", 1))
+        self.snapshot_dir = self.snapshot.cfg.directory if self.snapshot.enabled else None
 
     def set_dcp(self, size: int, rank: int):
         """Shard every sequence's KV over a DCP replica set of ``size`` ranks: the scheduler's
@@ -372,19 +373,10 @@ class ModelRunner:
             fb.positions3 = torch.from_numpy(np.ascontiguousarray(pos3)).to(self.device, non_blocking=True)
 
     def _snapshot(self, out: SchedulerOutput, lay: Layout, decode: bool, splits: int):
-        """Save one step's device inputs (the packed int32 buffer and its layout)."""
-        import os
-
-        if self._snap_n >= self.snapshot_max:
-            return
-        os.makedirs(self.snapshot_dir, exist_ok=True)
-        torch.save({"step": self._snap_n, "layout": dict(T=lay.T, B=lay.B, S=lay.S, W=lay.W, nblk=lay.nblk),
-                    "offsets": lay.off, "buffer": self.host_buf[:lay.total].clone(), "decode": decode,
-                    "num_splits": splits, "work_len": getattr(self, "_last_work_len", 0),
-                    "requests": [(s.req.request_id, s.start, s.num_tokens, s.samples, list(s.spec))
-                                 for s in out.scheduled]},
-                   os.path.join(self.snapshot_dir, f"step_{self._snap_n:06d}.pt"))
-        self._snap_n += 1
+        """Save one step's device inputs (the packed int32 buffer and its layout) when the
+        snapshot configuration selects it (snapshot/capture.py)."""
+        self.snapshot.pre_execute(out, lay, self.host_buf, decode, splits, getattr(self, "_last_work_len", 0),
+                                  self.model, self._last_prefill_rows)
 
     def _views(self, buf: torch.Tensor, lay: Layout, B: int, S: int, W: int, decode: bool, splits: int) -> tuple:
         o = lay.off
@@ -668,6 +660,8 @@ class ModelRunner:
         lay = Layout(out.num_tokens, B, S, self._max_work_for(out), self.max_blocks)
         _, decode, splits = self._pack(out, lay)
         W = self._last_work_len
+        if self.snapshot_dir:
+            self._snapshot(out, lay, decode, splits)
         dev = self.dev_buf[:lay.total]
         dev.copy_(self.host_buf[:lay.total], non_blocking=self.is_cuda)
         fb, _ = self._views(dev, lay, B, S, W, decode, splits)
