@@ -19,6 +19,7 @@ import torch
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 from vllm_neuron_b200 import ops  # noqa: E402
+from vllm_neuron_b200.ops import attention as A  # noqa: E402
 from vllm_neuron_b200.ops import linear as L  # noqa: E402
 
 _FLUSH = None
@@ -158,15 +159,18 @@ def bench_prefill_attention(tp: int):
         sl = torch.full((B,), S, dtype=torch.int32, device="cuda")
         qs = torch.arange(0, (B + 1) * S, S, dtype=torch.int32, device="cuda")
         q = torch.randn(B * S, Hq, D, device="cuda", dtype=torch.bfloat16)
-        w = ops.build_work(np.full(B, S), sl.cpu().numpy(), Hq // Hkv, Hkv)
-        work = torch.from_numpy(w.work).cuda()
         out = torch.empty_like(q)
-        fn = lambda: ops.paged_attention(q, kc, vc, bt, sl, qs, work, False, 1, 1 / math.sqrt(D), out=out)
-        t = timeit(fn)
         flops = 4.0 * B * S * S / 2 * Hq * D
-        rows.append({"op": "prefill_attention", "B": B, "S": S, "Hq": Hq, "ms": t,
-                     "tflops": flops / t / 1e9})
-        print(json.dumps(rows[-1]), flush=True)
+        # 64-row items run the mma.sync kernel, 128-row items the tcgen05 (TMEM) kernel
+        for pr in sorted({A.PREFILL_ROWS, A.prefill_rows(D, kc.dtype, bs, Hq // Hkv)}):
+            w = ops.build_work(np.full(B, S), sl.cpu().numpy(), Hq // Hkv, Hkv, prefill_rows=pr)
+            work = torch.from_numpy(w.work).cuda()
+            fn = lambda: ops.paged_attention(q, kc, vc, bt, sl, qs, work, False, 1, 1 / math.sqrt(D), out=out,
+                                             prefill_rows=pr)
+            t = timeit(fn)
+            rows.append({"op": "prefill_attention", "rows": pr, "B": B, "S": S, "Hq": Hq, "ms": t,
+                         "tflops": flops / t / 1e9})
+            print(json.dumps(rows[-1]), flush=True)
     return rows
 
 

@@ -46,11 +46,12 @@ def _case(dev, q_lens, ctx_lens, Hq, Hkv, bs=16, seed=0, window=0, sinks=False, 
         bt2[0, 0] = nb  # names the extra block, which is beyond the cache the kernel is told
         out = ops.paged_attention(q.to(dev), kc_big[:nb].to(dev), vc_big[:nb].to(dev), bt2.to(dev), sl.to(dev),
                                   qs.to(dev), torch.from_numpy(w.work).to(dev), False, 1, scale,
-                                  window=window, sinks=sk.to(dev) if sk is not None else None)
+                                  window=window, sinks=sk.to(dev) if sk is not None else None,
+                                  prefill_rows=rows)
         return out, ref
     out = ops.paged_attention(q.to(dev), kc.to(dev), vc.to(dev), bt.to(dev), sl.to(dev), qs.to(dev),
                               torch.from_numpy(w.work).to(dev), False, 1, scale, window=window,
-                              sinks=sk.to(dev) if sk is not None else None)
+                              sinks=sk.to(dev) if sk is not None else None, prefill_rows=rows)
     return out, ref
 
 
