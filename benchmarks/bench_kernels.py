@@ -21,6 +21,7 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 from vllm_neuron_b200 import ops  # noqa: E402
 from vllm_neuron_b200.ops import attention as A  # noqa: E402
 from vllm_neuron_b200.ops import linear as L  # noqa: E402
+from vllm_neuron_b200.ops._ext import ext  # noqa: E402
 
 _FLUSH = None
 
@@ -77,12 +78,19 @@ def bench_gemms(tp: int):
                 fn = lambda: L.gemm_accumulate(x, w, acc)
                 kind = "splitk_f32"
             t = timeit(fn)
+            extra = {}
+            if kind == "wide" and ext().gemm_2sm_enabled():
+                # the single-SM kernel on the same shape (the CTA-pair kernel serves M >= 512)
+                ext().gemm_2sm_set(False)
+                t1 = timeit(fn)
+                ext().gemm_2sm_set(True)
+                extra = {"one_sm_ms": t1, "one_sm_tflops": flops / t1 / 1e9}
             bytes_ = (M * K + N * K) * 2 + M * N * 2
             rows.append({
                 "op": f"gemm_{name}", "M": M, "N": N, "K": K, "kind": kind,
                 "ms": t, "tflops": flops / t / 1e9, "gbs": bytes_ / t / 1e6,
                 "cublas_ms": t_ref, "cublas_tflops": flops / t_ref / 1e9,
-                "speedup_vs_cublas": t_ref / t,
+                "speedup_vs_cublas": t_ref / t, **extra,
             })
             print(json.dumps(rows[-1]), flush=True)
     return rows

@@ -1069,6 +1069,9 @@ int64_t launch_count() { return g_launches.load(); }
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels of vllm_neuron_b200";
   m.def("gemm", &gemm);
+  m.def("gemm_2sm_set", [](bool on) { b200::gemm2sm_set(on); });
+  m.def("gemm_2sm_enabled", []() { return b200::gemm2sm_enabled(); });
+  m.def("gemm_2sm_pairs", []() { return b200::gemm2sm_pairs(); });
   m.def("gemm_sp", &gemm_sp);
   m.def("gemm_fp8", &gemm_fp8);
   m.def("quant_fp8", &quant_fp8);

@@ -72,6 +72,14 @@ struct GemmArgs {
 };
 
 void gemm_bf16_launch(const GemmArgs& args, cudaStream_t stream);
+// Two-SM (cta_group::2) kernel for the large dense bf16 shapes (gemm_2sm.cu): EPI_BF16 and
+// EPI_SILU_BF16, no split-K, M >= 512; gemm_bf16_launch routes eligible calls to it unless
+// VLLM_B200_GEMM_2SM=0.
+bool gemm2sm_enabled();
+void gemm2sm_set(bool on);  // process-wide switch (benchmarks and tests)
+int gemm2sm_pairs();        // co-resident CTA pairs the kernel launches
+bool gemm2sm_eligible(const GemmArgs& args);
+void gemm2sm_launch(const GemmArgs& args, cudaStream_t stream);
 CUtensorMap make_tmap_bf16_2d(const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld,
                               uint32_t box_inner, uint32_t box_outer, bool swizzle128);
 // Byte-element 2-D map (fp8 data); swizzle_bytes is 0, 64 or 128.

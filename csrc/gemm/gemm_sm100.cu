@@ -746,6 +746,10 @@ void gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
   if ((a.K * esz) % 16 != 0) throw std::invalid_argument("gemm: K rows must be multiples of 16 bytes");
   if ((a.lda * esz) % 16 != 0 || (a.ldb * esz) % 16 != 0)
     throw std::invalid_argument("gemm: row pitches must be multiples of 16 bytes");
+  if (gemm2sm_eligible(a)) {
+    gemm2sm_launch(a, stream);
+    return;
+  }
   const int bn = a.bn;
   const bool grouped = a.gtiles != nullptr;
   if (grouped && (a.splits > 1 || a.splits < 0 || a.num_groups < 1 || a.gmax < 1))
