@@ -49,8 +49,9 @@ struct PagedAttnParams {
   // Write unnormalised split partials (part_o / part_lse) even for one split and leave the
   // merge to the caller (DCP merges the partials of all ranks after exchanging them).
   int partial_out;
-  // Packed query rows per prefill work item: 64 (mma.sync kernel) or 128 (tcgen05 kernel,
-  // fmha_sm100.cu); 0 means 64.  The work list must have been built with the same value.
+  // Packed query rows per prefill work item: 64 (mma.sync kernel) or fmha_prefill_rows() = 256
+  // (tcgen05 kernel, fmha_sm100.cu); 0 means 64.  The work list must have been built with the
+  // same value.
   int prefill_rows;
 };
 
@@ -74,6 +75,7 @@ void paged_attention_launch(const PagedAttnParams& p, int num_work, int head_dim
 
 // tcgen05 prefill attention (fmha_sm100.cu): head_dim 128, bf16 cache, one split, 128-row work
 // items.
+int fmha_prefill_rows();  // packed rows per tcgen05 prefill work item
 bool fmha_prefill_supported(const PagedAttnParams& p, int head_dim);
 void fmha_prefill_launch(const PagedAttnParams& p, int num_work, cudaStream_t stream);
 

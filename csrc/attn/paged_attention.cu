@@ -587,15 +587,16 @@ void paged_attention_launch(const PagedAttnParams& p_in, int num_work, int head_
   const bool tma = decode && paged_decode_tma_supported(p, head_dim);
   // device split factors are a feature of the TMA decode path with the warp combine (<= 32)
   if (!tma || p.num_splits > 32 || p.partial_out) p.splits_dev = nullptr;
-  if (!decode && p.prefill_rows == 128) {
+  if (!decode && p.prefill_rows == fmha_prefill_rows()) {
     if (!fmha_prefill_supported(p, head_dim))
-      throw std::invalid_argument("paged_attention: 128-row prefill work needs the tcgen05 kernel's "
-                                  "conditions (head_dim 128, bf16 cache, one split, no DCP)");
+      throw std::invalid_argument("paged_attention: tcgen05 prefill work items need head_dim 128, a bf16 "
+                                  "cache, one split, no DCP and a block size dividing 128");
     fmha_prefill_launch(p, num_work, stream);
     return;
   }
   if (!decode && p.prefill_rows != 0 && p.prefill_rows != 64)
-    throw std::invalid_argument("paged_attention: prefill work items must hold 64 or 128 rows");
+    throw std::invalid_argument("paged_attention: prefill work items must hold 64 rows (mma.sync "
+                                "kernel) or " + std::to_string(fmha_prefill_rows()) + " (tcgen05 kernel)");
   if (tma) {
     paged_decode_tma_launch(p, num_work, head_dim, stream);
   } else if (head_dim == 128) {

@@ -317,11 +317,205 @@ __global__ void __launch_bounds__(256) rope_kv_write_kernel(const RopeKvParams p
   }
 }
 
+// Vectorised form for the common layouts (full-width neox rotation or interleaved pairs, 1-D
+// positions): lane l owns the D / 32 contiguous elements [l * PER, l * PER + PER) of a head, so
+// every access is one 4- to 32-byte vector; the neox partner (i, i + D / 2) sits in lane l ^ 16.
+// Each warp first loads all of its HPW heads, so HPW loads per lane are in flight at once --
+// the per-head form above waits one load latency per head, which bounds large prefill steps.
+namespace {
+template <int BYTES>
+__device__ __forceinline__ void ld_words(const void* src, uint32_t (&w)[BYTES / 4]) {
+  if constexpr (BYTES >= 16) {
+#pragma unroll
+    for (int i = 0; i < BYTES / 16; ++i) {
+      const uint4 u = reinterpret_cast<const uint4*>(src)[i];
+      w[4 * i] = u.x; w[4 * i + 1] = u.y; w[4 * i + 2] = u.z; w[4 * i + 3] = u.w;
+    }
+  } else if constexpr (BYTES == 8) {
+    const uint2 u = *reinterpret_cast<const uint2*>(src);
+    w[0] = u.x; w[1] = u.y;
+  } else {
+    w[0] = *reinterpret_cast<const uint32_t*>(src);
+  }
+}
+template <int BYTES>
+__device__ __forceinline__ void st_words(void* dst, const uint32_t (&w)[BYTES / 4]) {
+  if constexpr (BYTES >= 16) {
+#pragma unroll
+    for (int i = 0; i < BYTES / 16; ++i)
+      reinterpret_cast<uint4*>(dst)[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+  } else if constexpr (BYTES == 8) {
+    *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
+  } else {
+    *reinterpret_cast<uint32_t*>(dst) = w[0];
+  }
+}
+template <typename T, int N>
+__device__ __forceinline__ void ld_vec(const T* src, float (&v)[N]) {
+  if constexpr (sizeof(T) == 4) {
+    uint32_t w[N];
+    ld_words<4 * N>(src, w);
+#pragma unroll
+    for (int i = 0; i < N; ++i) v[i] = __uint_as_float(w[i]);
+  } else {
+    uint32_t w[N / 2];
+    ld_words<2 * N>(src, w);
+#pragma unroll
+    for (int i = 0; i < N / 2; ++i) {
+      const float2 f = unpack_bf16x2(w[i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  }
+}
+template <int N>
+__device__ __forceinline__ void st_vec_bf16(__nv_bfloat16* dst, const float (&v)[N], float mul) {
+  uint32_t w[N / 2];
+#pragma unroll
+  for (int i = 0; i < N / 2; ++i) w[i] = pack_bf16x2(v[2 * i] * mul, v[2 * i + 1] * mul);
+  st_words<N * 2>(dst, w);
+}
+template <typename T, int N>
+__device__ __forceinline__ void zero_vec(T* dst) {
+  uint32_t w[N * sizeof(T) / 4];
+#pragma unroll
+  for (int i = 0; i < (int)(N * sizeof(T) / 4); ++i) w[i] = 0u;
+  st_words<N * sizeof(T)>(dst, w);
+}
+}  // namespace
+
+constexpr int kRopeHeadsPerWarp = 4;
+
+template <typename TIN, int D>
+__global__ void __launch_bounds__(256) rope_kv_write_vec_kernel(const RopeKvParams p, TIN* qkv) {
+  pdl_trigger();
+  pdl_wait();
+  constexpr int PER = D / 32;
+  constexpr int HPW = kRopeHeadsPerWarp;
+  const int t = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nheads = p.Hq + 2 * p.Hkv;
+  const int h0 = ((int)blockIdx.y * (blockDim.x >> 5) + warp) * HPW;
+  if (h0 >= nheads) return;
+  const int pos = p.positions[t];
+  const long long slot = p.slot_mapping ? (long long)p.slot_mapping[t] : -1;
+  TIN* row = qkv + (long long)t * p.qkv_stride;
+  const int e0 = lane * PER;  // first element of this lane
+  float v[HPW][PER];
+#pragma unroll
+  for (int hh = 0; hh < HPW; ++hh)
+    if (h0 + hh < nheads) ld_vec<TIN, PER>(row + (long long)(h0 + hh) * D + e0, v[hh]);
+  // rotary coefficients of this lane's elements
+  const float* cs = p.cos_sin + (long long)pos * p.rot_dim;
+  float c[PER], sn[PER];
+  if (p.neox) {  // full width: element i pairs with i +- D / 2, frequency i mod D / 2
+    const int j0 = (lane & 15) * PER;
+#pragma unroll
+    for (int e = 0; e < PER; ++e) {
+      c[e] = cs[j0 + e];
+      sn[e] = cs[D / 2 + j0 + e];
+    }
+  } else {  // interleaved pairs (2j, 2j + 1) inside the lane; elements past rot_dim keep c = 1
+    const int half = p.rot_dim / 2;
+#pragma unroll
+    for (int e = 0; e < PER; ++e) {
+      const int i = e0 + e;
+      c[e] = i < p.rot_dim ? cs[i >> 1] : 1.f;
+      sn[e] = i < p.rot_dim ? cs[half + (i >> 1)] : 0.f;
+    }
+  }
+  const float qs = p.q_pos_beta != 0.f ? 1.f + p.q_pos_beta * logf(1.f + floorf((float)pos / p.q_pos_period)) : 1.f;
+#pragma unroll
+  for (int hh = 0; hh < HPW; ++hh) {
+    const int h = h0 + hh;
+    if (h >= nheads) break;
+    const bool is_q = h < p.Hq;
+    const bool is_k = !is_q && h < p.Hq + p.Hkv;
+    float (&x)[PER] = v[hh];
+    if (p.qkv_bias != nullptr) {
+      float b[PER];
+      ld_vec<float, PER>(p.qkv_bias + (long long)h * D + e0, b);
+#pragma unroll
+      for (int e = 0; e < PER; ++e) x[e] += b[e];
+    }
+    if ((is_q && p.q_norm_w) || (is_k && p.k_norm_w)) {
+      float ss = 0.f;
+#pragma unroll
+      for (int e = 0; e < PER; ++e) ss += x[e] * x[e];
+      ss = warp_sum(ss);
+      const float inv = rsqrtf(ss / (float)D + p.eps);
+      float w[PER];
+      ld_vec<__nv_bfloat16, PER>(is_q ? p.q_norm_w + e0 : p.k_norm_w + e0, w);
+#pragma unroll
+      for (int e = 0; e < PER; ++e) x[e] = __bfloat162float(__float2bfloat16(x[e] * inv * w[e]));
+    }
+    if (is_q || is_k) {
+      if (p.neox) {
+        const float sgn = lane < 16 ? -1.f : 1.f;
+#pragma unroll
+        for (int e = 0; e < PER; ++e) {
+          const float other = __shfl_xor_sync(0xffffffffu, x[e], 16);
+          x[e] = x[e] * c[e] + sgn * other * sn[e];
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < PER; e += 2) {
+          const float a = x[e], b = x[e + 1];
+          x[e] = a * c[e] - b * sn[e];
+          x[e + 1] = b * c[e + 1] + a * sn[e + 1];
+        }
+      }
+    }
+    if (is_q) {
+      st_vec_bf16<PER>(p.q_out + (long long)t * p.q_out_stride + (long long)h * D + e0, x, qs);
+    } else if (slot >= 0 && p.num_blocks > 0 && slot >= p.num_blocks * p.block_size) {
+      if (lane == 0) set_status(p.status, kBadIndex);  // slot past the cache: not written
+    } else if (slot >= 0) {
+      const int kvh = is_k ? h - p.Hq : h - p.Hq - p.Hkv;
+      const long long blk = slot / p.block_size, off = slot % p.block_size;
+      const long long idx = blk * p.kv_block_stride + ((long long)kvh * p.block_size + off) * D + e0;
+      if (p.kv_fp8) {
+        uint8_t* dst = reinterpret_cast<uint8_t*>(is_k ? p.k_cache : p.v_cache) + idx;
+        const float inv = is_k ? p.k_inv_scale : p.v_inv_scale;
+#pragma unroll
+        for (int e = 0; e < PER; ++e)
+          dst[e] = (uint8_t)__nv_cvt_float_to_fp8(x[e] * inv, __NV_SATFINITE, __NV_E4M3);
+      } else {
+        st_vec_bf16<PER>((is_k ? p.k_cache : p.v_cache) + idx, x, 1.f);
+      }
+    }
+    if (p.clear_input) zero_vec<TIN, PER>(row + (long long)h * D + e0);
+  }
+}
+
 void rope_kv_write_launch(const RopeKvParams& p, void* qkv, bool qkv_is_f32, int T,
                           cudaStream_t stream) {
   if (T == 0) return;
   if (p.positions3 != nullptr && !(p.neox && p.rot_dim == p.head_dim && p.head_dim >= 64))
     throw std::invalid_argument("rope_kv_write: multimodal RoPE needs full-width neox rotation");
+  const int esz = qkv_is_f32 ? 4 : 2;
+  const bool vec = p.positions3 == nullptr && (!p.neox || p.rot_dim == p.head_dim) && (p.rot_dim % 2) == 0 &&
+                   (p.qkv_stride * esz) % 16 == 0 && (p.q_out_stride * 2) % 16 == 0 &&
+                   (p.kv_block_stride * (p.kv_fp8 ? 1 : 2)) % 16 == 0;
+  if (vec) {
+    // 8 warps x kRopeHeadsPerWarp heads per CTA, grid (tokens, head groups)
+    const int per_cta = 8 * kRopeHeadsPerWarp;
+    const dim3 vgrid(T, (p.Hq + 2 * p.Hkv + per_cta - 1) / per_cta);
+#define B200_ROPE_VEC(D_)                                                                   \
+    if (p.head_dim == D_) {                                                                 \
+      if (qkv_is_f32)                                                                       \
+        launch_pdl(rope_kv_write_vec_kernel<float, D_>, vgrid, dim3(256), 0, stream, p,      \
+                   (float*)qkv);                                                            \
+      else                                                                                  \
+        launch_pdl(rope_kv_write_vec_kernel<__nv_bfloat16, D_>, vgrid, dim3(256), 0, stream, \
+                   p, (__nv_bfloat16*)qkv);                                                 \
+      return;                                                                               \
+    }
+    B200_ROPE_VEC(64)
+    B200_ROPE_VEC(128)
+    B200_ROPE_VEC(256)
+#undef B200_ROPE_VEC
+  }
   // one warp per head: 8 heads per CTA, grid (tokens, head groups)
   const dim3 grid(T, (p.Hq + 2 * p.Hkv + 7) / 8);
 #define B200_ROPE(D_)                                                                       \

@@ -1,11 +1,13 @@
 """tcgen05 prefill attention (csrc/attn/fmha_sm100.cu) against the fp32 oracle.
 
 Head dim 128 with a bf16 cache runs prefill and chunked-prefill steps on the tensor-core kernel
-(128 packed query rows per work item, S and O in TMEM, V transposed in shared memory).  Cases:
-GQA groups 4 and 8, several sequences with cached context (chunked prefill), sliding windows,
-learned sinks, block sizes 16 and 32, a query past a 64-token tile boundary and a single-token
-prefill among long ones.  Also checks the bounds guard: a block table entry beyond the cache is
-read as the null block and reported in the device status word.
+(256 packed query rows per work item as two 128-row Q tiles, 128-token KV tiles, S / P / O in
+TMEM, V read MN-major).  Cases: GQA groups 1, 4, 8 and 16, several sequences with cached context
+(chunked prefill), sliding windows (narrower than a tile and spanning several), learned sinks,
+block sizes 16, 32, 64 and 128, items whose second Q tile is empty, queries past a KV tile
+boundary, a single-token prefill among long ones and a 4k-token sequence.  Also checks the bounds
+guard: a block table entry beyond the cache is read as the null block and reported in the device
+status word.
 """
 import math
 
@@ -35,7 +37,7 @@ def _case(dev, q_lens, ctx_lens, Hq, Hkv, bs=16, seed=0, window=0, sinks=False, 
     sk = (torch.randn(Hq, generator=g) * 2).float() if sinks else None
     scale = 1 / math.sqrt(D)
     rows = ops.attention.prefill_rows(D, torch.bfloat16)
-    assert rows == 128
+    assert rows == 256
     w = ops.build_work(np.array(q_lens), np.array(seq_lens), Hq // Hkv, Hkv, head_dim=D, prefill_rows=rows)
     assert not w.decode
     ref = ops.paged_attention_ref(q, kc, vc, bt, sl, qs, scale, window, sk)
@@ -67,6 +69,11 @@ def _rel(a, b):
     ([250, 40], [0, 500], 16, 4, 32, 0, False),                  # block size 32
     ([300, 90], [0, 200], 64, 8, 16, 128, True),                 # sliding window + sinks
     ([1000], [2000], 32, 8, 16, 0, True),
+    ([20, 31], [0, 5], 32, 8, 16, 0, False),                     # second Q tile empty
+    ([513, 130], [0, 64], 8, 8, 64, 0, False),                   # G = 1, block size 64
+    ([96, 300], [10, 0], 64, 4, 128, 0, False),                  # G = 16, block size 128
+    ([700], [300], 32, 8, 16, 100, False),                       # window narrower than a KV tile
+    ([4096], [0], 32, 8, 16, 0, False),
 ])
 def test_fmha_prefill_matches_oracle(cuda_device, q_lens, ctx, Hq, Hkv, bs, window, sinks):
     out, ref = _case(cuda_device, q_lens, ctx, Hq, Hkv, bs=bs, window=window, sinks=sinks)

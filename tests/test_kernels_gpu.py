@@ -178,11 +178,17 @@ def test_add_rmsnorm(cuda_device, H, f32_in):
     assert _rel_err(out2, ref) < 1e-2
 
 
-@pytest.mark.parametrize("D,neox,qknorm,f32_in", [(128, True, False, False), (128, True, True, True),
-                                                  (64, True, False, True), (128, False, False, False),
-                                                  (256, True, True, False)])
-def test_rope_kv_write(cuda_device, D, neox, qknorm, f32_in):
-    T, Hq, Hkv, bs, nb = 20, 8, 2, 16, 8
+@pytest.mark.parametrize("D,neox,qknorm,f32_in,rot,T,Hq,Hkv", [
+    (128, True, False, False, None, 20, 8, 2), (128, True, True, True, None, 20, 8, 2),
+    (64, True, False, True, None, 20, 8, 2), (128, False, False, False, None, 20, 8, 2),
+    (256, True, True, False, None, 20, 8, 2),
+    (128, True, False, False, None, 300, 32, 8),   # two head groups per token (vector kernel)
+    (128, False, False, True, 64, 40, 8, 2),       # interleaved, partial rotary (vector kernel)
+    (128, True, False, False, 64, 40, 8, 2),       # neox, partial rotary (per-head kernel)
+])
+def test_rope_kv_write(cuda_device, D, neox, qknorm, f32_in, rot, T, Hq, Hkv):
+    bs, nb = 16, (T + 15) // 16 + 4
+    rot = rot or D
     dt = torch.float32 if f32_in else torch.bfloat16
     qkv = torch.randn(T, (Hq + 2 * Hkv) * D, device=cuda_device, dtype=dt)
     qkv_cpu = qkv.detach().cpu().clone()
@@ -190,19 +196,19 @@ def test_rope_kv_write(cuda_device, D, neox, qknorm, f32_in):
     slots = torch.randperm(nb * bs)[:T].to(torch.int32)
     slots[3] = -1
     slots = slots.to(cuda_device)
-    tab = ops.cos_sin_table(4096, D, 500000.0, device=cuda_device)
+    tab = ops.cos_sin_table(4096, rot, 500000.0, device=cuda_device)
     qn = torch.randn(D, device=cuda_device, dtype=torch.bfloat16) if qknorm else None
     kn = torch.randn(D, device=cuda_device, dtype=torch.bfloat16) if qknorm else None
     kc = torch.zeros(nb, Hkv, bs, D, device=cuda_device, dtype=torch.bfloat16)
     vc = torch.zeros_like(kc)
     q_out = torch.empty(T, Hq * D, device=cuda_device, dtype=torch.bfloat16)
     ops.rope_kv_write(qkv, pos, tab, Hq, Hkv, D, q_out, kc, vc, slots, qn, kn, 1e-6, neox=neox,
-                      clear_input=True)
+                      clear_input=True, rot_dim=rot)
     kc_r = torch.zeros(nb, Hkv, bs, D, dtype=torch.bfloat16)
     vc_r = torch.zeros_like(kc_r)
     q_r = torch.empty(T, Hq * D, dtype=torch.bfloat16)
     ops.rope_kv_write_ref(qkv_cpu, pos.cpu(), tab.cpu(), Hq, Hkv, D, q_r, kc_r, vc_r, slots.cpu(),
-                          qn.cpu() if qknorm else None, kn.cpu() if qknorm else None, 1e-6, D, neox)
+                          qn.cpu() if qknorm else None, kn.cpu() if qknorm else None, 1e-6, rot, neox)
     assert _rel_err(q_out.cpu(), q_r) < 1e-2
     assert _rel_err(kc.cpu(), kc_r) < 1e-2
     assert _rel_err(vc.cpu(), vc_r) < 1e-2

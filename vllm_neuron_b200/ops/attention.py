@@ -24,20 +24,21 @@ from ._ext import ext
 
 FP8_MAX = 448.0   # largest finite float8_e4m3fn value
 PREFILL_ROWS = 64
-PREFILL_ROWS_TC = 128  # work items of the tcgen05 prefill kernel (csrc/attn/fmha_sm100.cu)
+PREFILL_ROWS_TC = 256  # work items of the tcgen05 prefill kernel: two 128-row Q tiles (csrc/attn/fmha_sm100.cu)
 DECODE_ROWS = 16
 
 
 def prefill_rows(head_dim: int, kv_dtype, block_size: int = 16, group: int = 1, dcp_size: int = 1) -> int:
-    """Packed query rows per prefill work item: 128 when the tcgen05 kernel serves the step
-    (head_dim 128, bf16 cache, block size dividing its 64-token KV tile, GQA group dividing 128,
-    no DCP), else 64 for the mma.sync kernel.  The work list and the kernel must agree."""
+    """Packed query rows per prefill work item: 256 when the tcgen05 kernel serves the step
+    (head_dim 128, bf16 cache, block size dividing its 128-token KV tile, GQA group dividing
+    its 128-row Q tile, no DCP), else 64 for the mma.sync kernel.  The work list and the kernel
+    must agree."""
     import torch
 
     from .. import envs
 
     if (head_dim == 128 and kv_dtype == torch.bfloat16 and dcp_size <= 1 and block_size > 0
-            and block_size % 8 == 0 and 64 % block_size == 0 and group > 0 and 128 % group == 0
+            and block_size % 8 == 0 and 128 % block_size == 0 and group > 0 and 128 % group == 0
             and not envs.VLLM_B200_DISABLE_TC_ATTENTION):
         return PREFILL_ROWS_TC
     return PREFILL_ROWS
