@@ -264,13 +264,58 @@ def bench_deltanet(tp: int):
     return rows
 
 
+def profile_case(name: str):
+    """Run one kernel three times on one shape without timing (the target of an ncu capture:
+    ``ncu -k regex:<kernel> -s 1 -c 1 python benchmarks/bench_kernels.py --profile-case NAME``).
+
+    fmha       tcgen05 prefill attention, 2 x 4096 tokens, Llama-3-8B heads (fmha_prefill_kernel)
+    gemm2sm    gate/up + SwiGLU projection, M = 8192, N = 28672, K = 4096 (gemm2sm_kernel)
+    gemm_dec   decode gate/up projection, M = 64, stream-K fp32 reduction (gemm_bf16_kernel)
+    """
+    if name == "fmha":
+        Hq, Hkv, D, bs, B, S = 32, 8, 128, 16, 2, 4096
+        nblk = S // bs
+        nb = B * nblk + 1
+        kc = torch.randn(nb, Hkv, bs, D, device="cuda", dtype=torch.bfloat16)
+        vc = torch.randn_like(kc)
+        bt = (torch.randperm(nb - 1, device="cuda")[: B * nblk] + 1).view(B, nblk).to(torch.int32)
+        sl = torch.full((B,), S, dtype=torch.int32, device="cuda")
+        qs = torch.arange(0, (B + 1) * S, S, dtype=torch.int32, device="cuda")
+        q = torch.randn(B * S, Hq, D, device="cuda", dtype=torch.bfloat16)
+        pr = A.prefill_rows(D, kc.dtype, bs, Hq // Hkv)
+        w = ops.build_work(np.full(B, S), sl.cpu().numpy(), Hq // Hkv, Hkv, prefill_rows=pr)
+        work = torch.from_numpy(w.work).cuda()
+        out = torch.empty_like(q)
+        fn = lambda: ops.paged_attention(q, kc, vc, bt, sl, qs, work, False, 1, 1 / math.sqrt(D), out=out,
+                                         prefill_rows=pr)
+    elif name == "gemm2sm":
+        x = torch.randn(8192, 4096, device="cuda", dtype=torch.bfloat16)
+        w = torch.randn(28672, 4096, device="cuda", dtype=torch.bfloat16) * 0.02
+        out = torch.empty(8192, 14336, device="cuda", dtype=torch.bfloat16)
+        fn = lambda: L.gemm_silu(x, w, out=out)
+    elif name == "gemm_dec":
+        x = torch.randn(64, 4096, device="cuda", dtype=torch.bfloat16)
+        w = torch.randn(28672, 4096, device="cuda", dtype=torch.bfloat16) * 0.02
+        acc = torch.zeros(64, 28672, device="cuda", dtype=torch.float32)
+        fn = lambda: L.gemm_accumulate(x, w, acc)
+    else:
+        raise SystemExit(f"unknown profile case {name}")
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    print("profile case", name, "done", flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--profile-case", type=str, default=None, help="fmha | gemm2sm | gemm_dec (see profile_case)")
     ap.add_argument("--tp", type=int, default=1)
     ap.add_argument("--json", type=str, default=None)
     ap.add_argument("--only", type=str, default="gemm,decode,prefill,moe,deltanet")
     a = ap.parse_args()
     torch.manual_seed(0)
+    if a.profile_case:
+        return profile_case(a.profile_case)
     rows = []
     only = a.only.split(",")
     if "gemm" in only:
