@@ -53,12 +53,6 @@ struct PagedAttnParams {
   // (tcgen05 kernel, fmha_sm100.cu); 0 means 64.  The work list must have been built with the
   // same value.
   int prefill_rows;
-  // Decode split merge inside the TMA decode kernel: the warp that finishes the last non-empty
-  // split of a (work item, KV head) merges the partials into `out` (no separate combine
-  // launch).  combine_ctr[item * Hkv + kvh] counts finished splits; the merging warp resets it,
-  // so the counters are zero between launches.  Set by the launcher.
-  int fused_combine;
-  int* combine_ctr;
 };
 
 #ifdef __CUDACC__
@@ -82,8 +76,6 @@ void paged_attention_launch(const PagedAttnParams& p, int num_work, int head_dim
 // tcgen05 prefill attention (fmha_sm100.cu): head_dim 128, bf16 cache, one split, 128-row work
 // items.
 int fmha_prefill_rows();  // packed rows per tcgen05 prefill work item
-// True when a decode launch with these parameters merges its splits inside the decode kernel.
-bool paged_decode_merges_splits(const PagedAttnParams& p, int head_dim, bool decode);
 bool fmha_prefill_supported(const PagedAttnParams& p, int head_dim);
 void fmha_prefill_launch(const PagedAttnParams& p, int num_work, cudaStream_t stream);
 

@@ -580,11 +580,6 @@ static void combine_splits(const float* po, const float* pl, __nv_bfloat16* out,
   }
 }
 
-bool paged_decode_merges_splits(const PagedAttnParams& p, int head_dim, bool decode) {
-  return decode && paged_decode_tma_supported(p, head_dim) && p.num_splits > 1 && p.num_splits <= 32 &&
-         !p.partial_out && p.combine_ctr != nullptr && p.dcp_seq_lens == nullptr;
-}
-
 void paged_attention_launch(const PagedAttnParams& p_in, int num_work, int head_dim, bool decode,
                             cudaStream_t stream) {
   if (num_work == 0) return;
@@ -603,9 +598,7 @@ void paged_attention_launch(const PagedAttnParams& p_in, int num_work, int head_
     throw std::invalid_argument("paged_attention: prefill work items must hold 64 rows (mma.sync "
                                 "kernel) or " + std::to_string(fmha_prefill_rows()) + " (tcgen05 kernel)");
   if (tma) {
-    p.fused_combine = paged_decode_merges_splits(p, head_dim, decode) ? 1 : 0;
     paged_decode_tma_launch(p, num_work, head_dim, stream);
-    if (p.fused_combine) return;
   } else if (head_dim == 128) {
     decode ? launch_attn<128, true>(p, num_work, stream)
            : launch_attn<128, false>(p, num_work, stream);

@@ -97,10 +97,9 @@ __device__ __forceinline__ void mma16816_f16(float (&d)[4], const uint32_t (&a)[
 }
 
 struct Unit {
-  int b, row0, kvh, split, item;
+  int b, row0, kvh, split;
   int q_begin, kv_len, ctx0, rows_here, p_min, p_max;
   int s_lo, s_hi;  // tile range [s_lo, s_hi) of 16-token tiles
-  int n_nonempty;  // splits of this (item, KV head) that own at least one tile
 };
 
 // Last visible key (local index) of packed query i of unit x; under decode context
@@ -115,7 +114,6 @@ __device__ __forceinline__ Unit unit_info(const PagedAttnParams& p, int u, int n
   Unit x;
   const int per_item = p.Hkv * ns;
   const int item = u / per_item;
-  x.item = item;
   const int rem = u - item * per_item;
   x.kvh = rem / ns;
   x.split = rem - x.kvh * ns;
@@ -137,54 +135,10 @@ __device__ __forceinline__ Unit unit_info(const PagedAttnParams& p, int u, int n
   const int per = (t_hi - t_lo + ns - 1) / ns;
   x.s_lo = t_lo + x.split * per;
   x.s_hi = min(x.s_lo + per, t_hi);
-  x.n_nonempty = per > 0 ? (t_hi - t_lo + per - 1) / per : 0;
   return x;
 }
 
 }  // namespace
-
-// Merge the n non-empty split partials of unit x's query rows into `out` (one warp).  The
-// partials were written by other warps (other SMs): they are read through L2 (ld.global.cg)
-// after the counter handshake.
-template <int D>
-__device__ __forceinline__ void merge_unit_splits(const PagedAttnParams& p, const Unit& x, int n, int lane) {
-  constexpr int PER = D / 32;
-  const long long sstride = (long long)p.total_tokens * p.Hq;
-  for (int r = 0; r < x.rows_here; ++r) {
-    const int pr = x.row0 + r;
-    const int tok = x.q_begin + pr / p.G, head = x.kvh * p.G + pr % p.G;
-    const long long base = (long long)tok * p.Hq + head;
-    const float l = lane < n ? __ldcg(p.part_lse + lane * sstride + base) : -INFINITY;
-    const float mx = warp_max(l);
-    const float w = (l == -INFINITY) ? 0.f : exp2f(l - mx);
-    const float den = warp_sum(w);
-    float acc[PER];
-#pragma unroll
-    for (int e = 0; e < PER; ++e) acc[e] = 0.f;
-    for (int s0 = 0; s0 < n; s0 += 4) {
-      float ws[4];
-      float v[4][PER];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int sp = s0 + q;
-        ws[q] = __shfl_sync(0xffffffffu, w, sp < n ? sp : 0);
-        if (sp >= n) ws[q] = 0.f;
-        const float* src = p.part_o + ((sp < n ? sp : 0) * sstride + base) * D + lane * PER;
-#pragma unroll
-        for (int e = 0; e < PER; ++e) v[q][e] = ws[q] != 0.f ? __ldcg(src + e) : 0.f;
-      }
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-#pragma unroll
-        for (int e = 0; e < PER; ++e) acc[e] += ws[q] * v[q][e];
-    }
-    const float inv = den > 0.f ? 1.f / den : 0.f;
-    __nv_bfloat16* dst = p.out + (long long)tok * p.o_stride_t + (long long)head * D + lane * PER;
-#pragma unroll
-    for (int e = 0; e < PER; e += 2)
-      *reinterpret_cast<uint32_t*>(dst + e) = pack_bf16x2(acc[e] * inv, acc[e + 1] * inv);
-  }
-}
 
 template <int D, int STAGES, int kWarps, bool FP8>
 __global__ void __launch_bounds__(kWarps * 32, 1)
@@ -269,17 +223,6 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
       }
       const Unit x = unit_info(p, u, ns);
       if (x.s_lo >= x.s_hi) {
-        if (p.fused_combine) {
-          // merged in the kernel from the non-empty splits only; with none at all (nothing
-          // visible) split 0 writes the zero rows
-          if (x.n_nonempty == 0 && x.split == 0 && lane < x.rows_here) {
-            const int pr = x.row0 + lane;
-            __nv_bfloat16* dst = p.out + (long long)(x.q_begin + pr / p.G) * p.o_stride_t +
-                                 (long long)(x.kvh * p.G + pr % p.G) * D;
-            for (int e = 0; e < D; e += 8) *reinterpret_cast<uint4*>(dst + e) = make_uint4(0u, 0u, 0u, 0u);
-          }
-          continue;
-        }
         // empty split: its partial carries no weight in the combine
         if (!direct && lane < x.rows_here) {
           const int pr = x.row0 + lane;
@@ -548,20 +491,6 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
           const float mu = m_r[h] == -INFINITY ? 0.f : m_r[h];
           p.part_lse[rowi] = l_r[h] > 0.f ? mu + log2f(l_r[h]) : -INFINITY;
         }
-      }
-    }
-    if (!direct && p.fused_combine) {
-      // the warp that finishes the last non-empty split of (item, KV head) merges them
-      __threadfence();
-      __syncwarp();
-      int* ctr = p.combine_ctr + (long long)x.item * p.Hkv + x.kvh;
-      int prev = 0;
-      if (lane == 0) prev = atomicAdd(ctr, 1);
-      prev = __shfl_sync(FULL, prev, 0);
-      if (prev == x.n_nonempty - 1) {
-        __threadfence();
-        merge_unit_splits<D>(p, x, x.n_nonempty, lane);
-        if (lane == 0) *ctr = 0;
       }
     }
   }

@@ -40,10 +40,8 @@ uint32_t* status_word() {
   return p;
 }
 
-// Unit counters of the persistent decode attention kernel, one pair per device, followed by
-// kDecodeCombineCtrs split-merge counters (zeroed once; each launch's last warp resets the
-// pair and each merging warp its counter).
-constexpr int kDecodeCombineCtrs = 1 << 16;
+// Unit counters of the persistent decode attention kernel, one pair per device (zeroed once;
+// each launch's last warp resets them).
 int* decode_sched_words() {
   static std::mutex mu;
   static std::unordered_map<int, int*> words;
@@ -53,9 +51,8 @@ int* decode_sched_words() {
   auto it = words.find(dev);
   if (it != words.end()) return it->second;
   int* p = nullptr;
-  const size_t bytes = (2 + kDecodeCombineCtrs) * sizeof(int);
-  TORCH_CHECK(cudaMalloc(&p, bytes) == cudaSuccess, "decode counter allocation failed");
-  TORCH_CHECK(cudaMemset(p, 0, bytes) == cudaSuccess, "decode counter init failed");
+  TORCH_CHECK(cudaMalloc(&p, 2 * sizeof(int)) == cudaSuccess, "decode counter allocation failed");
+  TORCH_CHECK(cudaMemset(p, 0, 2 * sizeof(int)) == cudaSuccess, "decode counter init failed");
   words[dev] = p;
   return p;
 }
@@ -79,8 +76,7 @@ void check_launch(const char* what, int kernels = 1) {
 
 // out = A @ B^T with the given epilogue.  A [M, K], B [N, K], both K-contiguous bf16.
 void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, int64_t epi, int64_t bn,
-          int64_t splits, int64_t group_m, int64_t max_ctas, int64_t fin_mode,
-          c10::optional<at::Tensor> fin_ctr, c10::optional<at::Tensor> fin_out) {
+          int64_t splits, int64_t group_m, int64_t max_ctas) {
   CHECK_CUDA(a);
   CHECK_CUDA(b);
   CHECK_CUDA(out);
@@ -108,18 +104,6 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, int64_t epi
   g.group_m = (int)group_m;
   g.max_ctas = (int)max_ctas;
   g.status = status_word();
-  if (fin_mode != 0) {
-    TORCH_CHECK(fin_ctr.has_value() && fin_out.has_value(), "gemm: a finisher needs counters and an output");
-    TORCH_CHECK(fin_ctr->scalar_type() == at::kInt && fin_ctr->is_cuda() && fin_ctr->numel() >= g.M / 256,
-                "gemm: finisher counters must be int32 CUDA, one per 256 weight rows");
-    CHECK_BF16(*fin_out);
-    TORCH_CHECK(fin_out->stride(1) == 1 && fin_out->size(0) >= g.N && fin_out->size(1) >= g.M / 2,
-                "gemm: finisher output must be [tokens, rows / 2] with contiguous rows");
-    g.fin_mode = (int)fin_mode;
-    g.fin_ctr = fin_ctr->data_ptr<int>();
-    g.fin_out = fin_out->data_ptr();
-    g.fin_ld = fin_out->stride(0);
-  }
   if (g.M == 0 || g.N == 0) return;
   b200::gemm_bf16_launch(g, cur_stream());
   check_launch("gemm");
@@ -446,10 +430,8 @@ void paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::T
     p.sched = decode_sched_words();
   }
   const int num_work = (int)work.size(0);
-  if (p.sched != nullptr && (long long)num_work * p.Hkv <= kDecodeCombineCtrs) p.combine_ctr = p.sched + 2;
   b200::paged_attention_launch(p, num_work, D, decode, cur_stream());
-  check_launch("paged_attention",
-               num_work == 0 ? 0 : (num_splits > 1 && !partial_out && !b200::paged_decode_merges_splits(p, D, decode) ? 2 : 1));
+  check_launch("paged_attention", num_work == 0 ? 0 : (num_splits > 1 && !partial_out ? 2 : 1));
 }
 
 // Merge split partials part_o [S, T, Hq, D] / part_lse [S, T, Hq] into out [T, Hq, D] bf16.
@@ -1086,9 +1068,7 @@ int64_t launch_count() { return g_launches.load(); }
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels of vllm_neuron_b200";
-  m.def("gemm", &gemm, py::arg("a"), py::arg("b"), py::arg("out"), py::arg("epi"), py::arg("bn"),
-        py::arg("splits"), py::arg("group_m"), py::arg("max_ctas"), py::arg("fin_mode") = 0,
-        py::arg("fin_ctr") = py::none(), py::arg("fin_out") = py::none());
+  m.def("gemm", &gemm);
   m.def("gemm_2sm_set", [](bool on) { b200::gemm2sm_set(on); });
   m.def("gemm_2sm_enabled", []() { return b200::gemm2sm_enabled(); });
   m.def("gemm_2sm_pairs", []() { return b200::gemm2sm_pairs(); });

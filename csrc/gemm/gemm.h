@@ -69,20 +69,7 @@ struct GemmArgs {
   // (lower k in the low nibble), rows of K / 2 bytes (lda / ldb in bytes), with one e8m0 scale
   // byte per 32 elements: w_scales8 [w_scale_rows][w_scale_ld] (one row per weight row).
   const uint8_t* w_scales8 = nullptr;
-  // EPI_F32_RED_T finisher (swapped-operand decode GEMMs with split-K or stream-K): when the
-  // last contribution to a tile group has been reduced into `out`, the warp that added it
-  // applies the group's epilogue op.  fin_mode GEMM_FIN_SILU: weight rows interleave 128 gate
-  // and 128 up rows; group j = tiles (2j, 2j + 1); fin_out[n, 128 j + c] =
-  // silu(out[n, 256 j + c]) * out[n, 256 j + 128 + c] (bf16, row pitch fin_ld), and the group's
-  // fp32 columns of `out` are zeroed.  fin_ctr: one int per group, zero before the launch and
-  // left zero by the finisher.
-  int fin_mode = 0;
-  int* fin_ctr = nullptr;
-  void* fin_out = nullptr;
-  long long fin_ld = 0;
 };
-
-enum GemmFinisher : int { GEMM_FIN_NONE = 0, GEMM_FIN_SILU = 1 };
 
 void gemm_bf16_launch(const GemmArgs& args, cudaStream_t stream);
 // Two-SM (cta_group::2) kernel for the large dense bf16 shapes (gemm_2sm.cu): EPI_BF16 and

@@ -76,33 +76,7 @@ struct GemmParams {
   const float* wsc;
   int wsc_ld, wsc_rows;
   const uint8_t* wsc8;  // MXFP4: e8m0 scale bytes [wsc_rows][wsc_ld], one per 32 elements
-  // EPI_F32_RED_T finisher (GemmArgs::fin_*)
-  int fin_mode;
-  int* fin_ctr;
-  __nv_bfloat16* fin_out;
-  long long fin_ld;
 };
-
-// SwiGLU finisher of group j (see GemmArgs::fin_mode): one warp, lane l owns columns
-// l, l + 32, l + 64, l + 96 of the group's 128 outputs.  The reduced sums were written by other
-// CTAs' reductions: they are read through L2.
-__device__ __forceinline__ void gemm_fin_silu(const GemmParams& p, int j, int lane) {
-  float* acc = reinterpret_cast<float*>(p.out);
-  const int tokens = p.N;
-#pragma unroll 1
-  for (int n = 0; n < tokens; ++n) {
-    float* g = acc + (long long)n * p.ldo + (long long)j * 256;
-    __nv_bfloat16* o = p.fin_out + (long long)n * p.fin_ld + (long long)j * 128;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int c = lane + 32 * q;
-      const float gv = __ldcg(g + c), uv = __ldcg(g + 128 + c);
-      o[c] = __float2bfloat16(gv / (1.0f + __expf(-gv)) * uv);
-      g[c] = 0.f;
-      g[128 + c] = 0.f;
-    }
-  }
-}
 
 // Bounded wait until a monotonic counter (written by a peer with a system-scope release)
 // reaches `target`; returns at once once the status word is set (peers out of step).
@@ -274,7 +248,6 @@ __global__ void __launch_bounds__(W8 ? 320 : 192, 1)
   uint32_t* tmem_base_smem = reinterpret_cast<uint32_t*>(tempty_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_smem + 1);
   unsigned int* rs_arrivals = tmem_base_smem + 2;  // epilogue threads done with their RS stores
-  unsigned int* fin_arrivals = tmem_base_smem + 3; // epilogue warps done with a segment (finisher)
 
   const int warp = warp_id();
   const int lane = lane_id();
@@ -296,7 +269,6 @@ __global__ void __launch_bounds__(W8 ? 320 : 192, 1)
     }
     *abort_flag = 0;
     *rs_arrivals = 0u;
-    *fin_arrivals = 0u;
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -662,34 +634,6 @@ __global__ void __launch_bounds__(W8 ? 320 : 192, 1)
           }
         }
       }
-      if constexpr (EPI == EPI_F32_RED_T) {
-        if (p.fin_mode == GEMM_FIN_SILU) {
-          // Each warp fences its reductions and arrives on a shared-memory counter (no
-          // blocking barrier: a warp that left early on a failed wait cannot stall the
-          // others); the segment's last warp adds the segment's k-blocks to the group counter
-          // and, when that completes the group, applies the finisher.
-          __threadfence();
-          __syncwarp();
-          unsigned int prev = 0;
-          if (lane == 0) prev = atomicAdd(fin_arrivals, 1u);
-          prev = __shfl_sync(0xffffffffu, prev, 0);
-          if (prev == 4u * (unsigned int)(t_local + 1) - 1u) {
-            const int grp = mb >> 1;
-            int done = 0;
-            if (lane == 0) {
-              __threadfence();
-              const int add = k1 - k0;
-              done = (atomicAdd(p.fin_ctr + grp, add) + add == 2 * p.num_k_blocks) ? 1 : 0;
-            }
-            done = __shfl_sync(0xffffffffu, done, 0);
-            if (done) {
-              __threadfence();
-              gemm_fin_silu(p, grp, lane);
-              if (lane == 0) p.fin_ctr[grp] = 0;
-            }
-          }
-        }
-      }
       if constexpr (EPI == EPI_BF16_RS) {
         // Every epilogue thread fences its own peer stores of this tile and arrives on a
         // shared-memory counter; the 128th arrival raises the owners' counters (no blocking
@@ -880,14 +824,6 @@ void gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
   p.out = a.out;
   p.ldo = a.ldo;
   p.status = a.status;
-  p.fin_mode = a.fin_mode;
-  p.fin_ctr = a.fin_ctr;
-  p.fin_out = reinterpret_cast<__nv_bfloat16*>(a.fin_out);
-  p.fin_ld = a.fin_ld;
-  if (a.fin_mode == GEMM_FIN_SILU &&
-      (a.epi != EPI_F32_RED_T || grouped || a.fin_ctr == nullptr || a.fin_out == nullptr || a.M % 256 != 0))
-    throw std::invalid_argument("gemm: the SwiGLU finisher needs EPI_F32_RED_T, counters, an output and "
-                                "gate/up rows in 256-row groups");
   const long long tiles = grouped ? (long long)a.gmax * p.num_n_blocks
                                   : (long long)p.num_m_blocks * p.num_n_blocks * p.splits;
   int grid = num_sms_cached();

@@ -176,8 +176,6 @@ class LlamaForCausalLM(torch.nn.Module):
         self.acc_qkv = torch.zeros(max_dec, self.qkv_out, dtype=torch.float32, device=d)
         self.acc_h = torch.zeros(max_dec, self.H, dtype=torch.float32, device=d)
         self.acc_gu = torch.zeros(max_dec, 2 * self.I, dtype=torch.float32, device=d)
-        # per 256 gate/up rows: counters of the fused SwiGLU finisher (zero between launches)
-        self.silu_ctr = torch.zeros(max(1, 2 * self.I // 256), dtype=torch.int32, device=d)
         self.ws_logits_x = torch.zeros(max_seqs, self.H, dtype=bf, device=d)
         self.ws_logits = torch.zeros(max_seqs, self.V_local, dtype=bf, device=d)
         self.attn_splits_max = 32
@@ -502,11 +500,8 @@ class LlamaForCausalLM(torch.nn.Module):
         """Dense SwiGLU MLP; leaves ``x = nxt_norm(res += mlp(x))``."""
         if small:
             acc = self.acc_gu[:T]
-            if self.silu_blk == L.SILU_BLOCK:
-                act = L.gemm_accumulate_silu(x, ly.gate_up, acc, self.ws_act[:T], self.silu_ctr)
-            else:
-                L.gemm_accumulate(x, ly.gate_up, acc)
-                act = ops.silu_mul(acc, out=self.ws_act[:T], blk=self.silu_blk, clear_input=True)
+            L.gemm_accumulate(x, ly.gate_up, acc)
+            act = ops.silu_mul(acc, out=self.ws_act[:T], blk=self.silu_blk, clear_input=True)
             acc = self.acc_h[:T]
             L.gemm_accumulate(act, ly.down, acc)
             self._allreduce_norm(acc, res, nxt_norm, x, fused)

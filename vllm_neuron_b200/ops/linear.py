@@ -379,36 +379,6 @@ def gemm_accumulate(x: torch.Tensor, w: torch.Tensor, acc: torch.Tensor,
     return acc
 
 
-GEMM_FIN_SILU = 1
-
-
-def gemm_accumulate_silu(x: torch.Tensor, w_gu: torch.Tensor, acc: torch.Tensor, out: torch.Tensor,
-                         ctr: torch.Tensor, splits: int | None = None) -> torch.Tensor:
-    """Decode-size fused SwiGLU projection: ``out = silu(x @ g^T) * (x @ u^T)`` (bf16) with
-    ``w_gu`` interleaving gate/up rows in blocks of ``SILU_BLOCK``.  The split-K / stream-K fp32
-    sums go through ``acc`` (zero on entry, left zero); the CTA warp that adds the last
-    contribution to a gate/up block pair applies SwiGLU for it, so no separate activation
-    kernel runs.  ``ctr``: int32 zeros, one per 256 weight rows (left zero).  Other weight
-    formats and the CPU take the unfused path."""
-    M, K = x.shape
-    N = w_gu.shape[0]
-    fusable = (x.is_cuda and isinstance(w_gu, torch.Tensor) and w_gu.dtype == torch.bfloat16 and
-               M <= SKINNY_MAX and N % (2 * SILU_BLOCK) == 0 and not _lib(x, w_gu))
-    if not fusable:
-        gemm_accumulate(x, w_gu, acc, splits)
-        from .activation import silu_mul
-
-        return silu_mul(acc[:M], out=out[:M], blk=SILU_BLOCK, clear_input=True)
-    if splits is None:
-        tiles = math.ceil(N / 128)
-        sms = num_sms(x.device)
-        s = pick_splits(N, K, sms) if tiles < sms else -1
-    else:
-        s = splits
-    ext().gemm(w_gu, x, acc, EPI_F32_RED_T, skinny_bn(M), s, 0, 0, GEMM_FIN_SILU, ctr, out)
-    return out
-
-
 def gemm_silu(x: torch.Tensor, w_gu: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """Fused ``silu(x @ g^T) * (x @ u^T)`` where ``w_gu`` interleaves gate/up rows in blocks of
     ``SILU_BLOCK`` (see :func:`interleave_gate_up`)."""
