@@ -220,6 +220,8 @@ def build_llm(cfg, args, world: int, sp_on: bool, baseline: bool):
     max_len = IN + OUT + 16
     blocks = P * ((max_len + 15) // 16) + 64
     opts = {"sequence_parallel": sp_on}
+    if sp_on and not baseline and args.fused_sp:
+        opts["fused_sp"] = True
     if baseline:  # NCCL collectives + cuBLAS projections, same engine, kernels and schedule otherwise
         opts.update(fused_comm=False, use_cublas_baseline=True)
     return LLM(cfg, tensor_parallel_size=world, max_num_seqs=P, max_model_len=max_len,
@@ -246,6 +248,9 @@ def main():
     ap.add_argument("--baseline-steps", type=int, default=5,
                     help="timed waves of the NCCL + cuBLAS build (at most --steps)")
     ap.add_argument("--layers", type=int, default=None, help="debug only: fewer layers (invalid for reporting)")
+    ap.add_argument("--fused-sp", action="store_true",
+                    help="sequence-parallel prefill on the fused GEMM -> reduce-scatter / all-gather -> GEMM "
+                         "kernels over NVLink peer memory (default: NCCL collectives)")
     ap.add_argument("--sp", choices=["auto", "on", "off"], default="auto",
                     help="sequence-parallel prefill (auto: on when N > 1)")
     args = ap.parse_args()
