@@ -184,7 +184,8 @@ def bench_prefill_attention(tp: int):
 
 def bench_moe(tp: int):
     """GPT-OSS-20B expert block (32 experts top-4, hidden 2880, FFN 2880) at decode batch sizes:
-    bf16 grouped tcgen05 GEMMs against the MXFP4 decode kernel (same routing, same weights),
+    bf16 grouped tcgen05 GEMMs, the MXFP4 mma.sync decode kernel and the MXFP4 tcgen05 GEMM
+    (swapped grouped mode up to 64 tokens, W4A16 grouped above) on the same routing and weights,
     each block replayed from a CUDA graph.  The weight bandwidth counts only the active experts'
     weight bytes (router, routing and combine time included in the denominator)."""
     from vllm_neuron_b200.models.gpt_oss import _quant_experts, dequant_mxfp4
@@ -197,15 +198,17 @@ def bench_moe(tp: int):
     dn_b, dn_s = _quant_experts(torch.randn(E, H, I, device=dev, generator=g) * I ** -0.5)
     w_gu, w_dn = dequant_mxfp4(gu_b, gu_s), dequant_mxfp4(dn_b, dn_s)
     fp4_gu, fp4_dn = M.pack_mxfp4(gu_b, gu_s), M.pack_mxfp4(dn_b, dn_s)
+    mx_gu, mx_dn = L.MXFP4Weight.from_blocks(gu_b, gu_s), L.MXFP4Weight.from_blocks(dn_b, dn_s)
     rw = (torch.randn(E, H, device=dev, generator=g) * 0.05).to(torch.bfloat16)
     ws = M.MoEWorkspace.create(128, k, E, E, H, I, dev)
     rows = []
     for T in (1, 8, 32, 64, 128):
         x = torch.randn(T, H, device=dev, generator=g).to(torch.bfloat16)
 
-        def graph(fp4: bool):
+        def graph(fp4: bool, tc: bool = False):
             kw = dict(fp4_gu=fp4_gu, fp4_down=fp4_dn, fp4_max_tokens=1 << 20) if fp4 else {}
-            run = lambda: M.moe_block(x, rw, w_gu, w_dn, k, M.ROUTE_TOPK_SOFTMAX, act=M.ACT_GPTOSS, ws=ws, **kw)
+            wg, wd = (mx_gu, mx_dn) if tc else (w_gu, w_dn)
+            run = lambda: M.moe_block(x, rw, wg, wd, k, M.ROUTE_TOPK_SOFTMAX, act=M.ACT_GPTOSS, ws=ws, **kw)
             run()  # compile-time setup (shared-memory opt-in) outside the capture
             torch.cuda.synchronize()
             gr = torch.cuda.CUDAGraph()
@@ -216,13 +219,15 @@ def bench_moe(tp: int):
         # decode replays the block from a CUDA graph; time it the same way (no host gaps)
         t_bf16 = timeit(graph(False))
         t_fp4 = timeit(graph(True))
+        t_tc = timeit(graph(False, tc=True))
         active = int(torch.unique(ws.ids[:T]).numel())
         fp4_bytes = active * (fp4_gu[0].numel() + fp4_dn[0].numel())
         bf16_bytes = active * (w_gu[0].numel() + w_dn[0].numel()) * 2
         r = {"kernel": "moe_block_gptoss", "T": T, "tp": tp, "active_experts": active,
-             "bf16_us": t_bf16 * 1e3, "fp4_us": t_fp4 * 1e3,
+             "bf16_us": t_bf16 * 1e3, "fp4_mma_sync_us": t_fp4 * 1e3, "fp4_tcgen05_us": t_tc * 1e3,
              "bf16_weight_GBs": bf16_bytes / (t_bf16 * 1e-3) / 1e9,
-             "fp4_weight_GBs": fp4_bytes / (t_fp4 * 1e-3) / 1e9}
+             "fp4_mma_sync_weight_GBs": fp4_bytes / (t_fp4 * 1e-3) / 1e9,
+             "fp4_tcgen05_weight_GBs": fp4_bytes / (t_tc * 1e-3) / 1e9}
         print(json.dumps(r), flush=True)
         rows.append(r)
     return rows
