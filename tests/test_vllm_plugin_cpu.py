@@ -29,7 +29,11 @@ def test_register(monkeypatch):
         assert "vllm.platform_plugins" in f.read()
 
 
-def test_vllm_engine_through_b200_worker(tmp_path):
+@pytest.mark.parametrize("async_sched", [False, True])
+def test_vllm_engine_through_b200_worker(tmp_path, async_sched):
+    """vLLM's LLM on the B200 worker equals the framework's own engine (greedy), with vLLM's
+    synchronous and asynchronous scheduling (the worker then launches each step before the
+    previous one's tokens are back, reading them on the device)."""
     (tmp_path / "config.json").write_text(json.dumps(CFG))
     script = textwrap.dedent(f"""
         import json, os, sys
@@ -45,7 +49,8 @@ def test_vllm_engine_through_b200_worker(tmp_path):
         prompts.append(prompts[0][:20] + [5, 6, 7])  # shares a cached prefix block with prompt 0
         llm = LLM(model={str(tmp_path)!r}, skip_tokenizer_init=True, dtype="float32", max_model_len=256,
                   max_num_seqs=4, max_num_batched_tokens=64, load_format="dummy", seed=0, block_size=16,
-                  enforce_eager=True)
+                  enforce_eager=True, async_scheduling={async_sched!r})
+        assert llm.llm_engine.vllm_config.scheduler_config.async_scheduling == {async_sched!r}
         outs = llm.generate([{{"prompt_token_ids": p}} for p in prompts],
                             SamplingParams(max_tokens=12, temperature=0.0, ignore_eos=True))
         got = [list(o.outputs[0].token_ids) for o in outs]

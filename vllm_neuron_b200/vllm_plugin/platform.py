@@ -163,10 +163,8 @@ class B200Platform(Platform):
             raise ValueError("pipeline parallelism is not supported by the B200 platform")
         if par.distributed_executor_backend not in ("mp", "uni"):
             par.distributed_executor_backend = "uni" if par.world_size == 1 else "mp"
-        sched = vllm_config.scheduler_config
-        if getattr(sched, "async_scheduling", False):
-            log.info("async scheduling is replaced by the worker's synchronous step")
-            sched.async_scheduling = False
+        # vLLM's asynchronous scheduling is served: the worker launches each step with the
+        # previous step's tokens read on the device and returns AsyncModelRunnerOutput
         comp = vllm_config.compilation_config
         with contextlib.suppress(Exception):
             from vllm.config import CompilationMode, CUDAGraphMode

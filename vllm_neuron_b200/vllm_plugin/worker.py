@@ -53,6 +53,52 @@ def convert_sampling_params(sp) -> SamplingParams:
         seed=sp.seed, max_tokens=sp.max_tokens, ignore_eos=True, logprobs=getattr(sp, "logprobs", None))
 
 
+def _async_output_base():
+    try:
+        from vllm.v1.outputs import AsyncModelRunnerOutput
+
+        return AsyncModelRunnerOutput
+    except ImportError:  # pragma: no cover - older vLLM
+        return object
+
+
+class _StepOutput(_async_output_base()):
+    """One launched step's ModelRunnerOutput, built when its tokens are back on the host."""
+
+    def __init__(self, handle, req_ids: list[str], samples: list[bool], want_lp: bool):
+        self.handle, self.req_ids, self.samples, self.want_lp = handle, req_ids, samples, want_lp
+
+    def get_output(self) -> ModelRunnerOutput:
+        toks, lps = self.handle.result()
+        n = len(self.req_ids)
+        want_lp = self.want_lp
+        lp_ids = np.zeros((n, 1), dtype=np.int32) if want_lp else None
+        lp_val = np.zeros((n, 1), dtype=np.float32) if want_lp else None
+        lp_rank = np.zeros(n, dtype=np.int32) if want_lp else None
+        ranks = self.handle.ranks if want_lp else None
+        sampled, row = [], 0
+        for i, s in enumerate(self.samples):
+            if s:
+                t = int(toks[row])
+                if want_lp:
+                    lp_ids[i, 0] = t
+                    lp_val[i, 0] = float(lps[row])
+                    lp_rank[i] = int(ranks[row])
+                row += 1
+                sampled.append([t])
+            else:
+                sampled.append([])
+        logprobs = None
+        if want_lp:
+            from vllm.v1.outputs import LogprobsLists
+
+            logprobs = LogprobsLists(lp_ids, lp_val, lp_rank)
+        return ModelRunnerOutput(req_ids=list(self.req_ids),
+                                 req_id_to_index={rid: i for i, rid in enumerate(self.req_ids)},
+                                 sampled_token_ids=sampled, logprobs=logprobs, prompt_logprobs_dict={},
+                                 pooler_output=[])
+
+
 class B200Worker(WorkerBase):
     def __init__(self, vllm_config, local_rank: int, rank: int, distributed_init_method: str,
                  is_driver_worker: bool = False, **kwargs):
@@ -62,6 +108,8 @@ class B200Worker(WorkerBase):
         self.model = None
         self.runner = None
         self._profiler = None
+        # vLLM's asynchronous scheduling: outputs are returned as AsyncModelRunnerOutput
+        self.async_scheduling = bool(getattr(vllm_config.scheduler_config, "async_scheduling", False))
 
     # ---------------------------------------------------------------- start-up
     def init_device(self) -> None:
@@ -168,7 +216,9 @@ class B200Worker(WorkerBase):
                 r.block_ids = list(nb[0]) if nb else []
                 toks = cd.all_token_ids.get(rid) if cd.all_token_ids else None
                 if toks is not None:
+                    # every token is known on the host again (recompute after preemption)
                     r.output_token_ids = list(toks[len(r.prompt_token_ids):])
+                    r.num_pending = 0
             elif nb is not None:
                 r.block_ids.extend(nb[0])
             r.num_computed_tokens = cd.num_computed_tokens[i]
@@ -198,7 +248,16 @@ class B200Worker(WorkerBase):
                 s += 1
         return torch.from_numpy(full)
 
-    def sample_tokens(self, grammar_output) -> ModelRunnerOutput:
+    def sample_tokens(self, grammar_output):
+        """Launch the pending step and return its output -- at once (synchronous scheduling) or
+        as an ``AsyncModelRunnerOutput`` (vLLM's asynchronous scheduling, which schedules the
+        next step before this one's tokens are back).
+
+        All request state moves at launch time: the scheduled tokens count as computed and each
+        sampled token counts as pending.  Sampled tokens are never appended on the host: a
+        request's next input token is read on the device from its slot (the runner's
+        ``-(slot + 1)`` ids), so steps can be launched back to back.  The output object only
+        reads this step's host buffer, so vLLM may resolve it from another thread."""
         so, self._pending = self._pending, None
         if so is None:
             return EMPTY_MODEL_RUNNER_OUTPUT
@@ -211,36 +270,18 @@ class B200Worker(WorkerBase):
         out.num_tokens = so.total_num_scheduled_tokens
         want_lp = any(sr.samples and sr.req.sampling_params.logprobs is not None for sr in out.scheduled)
         handle = self.runner.launch(out, want_lp, self._bitmask(out, grammar_output), want_ranks=want_lp)
-        toks, lps = handle.result()
-        req_ids, sampled = [], []
-        row = 0
-        n = len(out.scheduled)
-        lp_ids = np.zeros((n, 1), dtype=np.int32) if want_lp else None
-        lp_val = np.zeros((n, 1), dtype=np.float32) if want_lp else None
-        lp_rank = np.zeros(n, dtype=np.int32) if want_lp else None
-        for i, sr in enumerate(out.scheduled):
+        req_ids, samples = [], []
+        for sr in out.scheduled:
             r = sr.req
             req_ids.append(r.request_id)
+            samples.append(sr.samples)
             r.num_computed_tokens = sr.start + sr.num_tokens
             if sr.samples:
-                t = int(toks[row])
-                if want_lp:
-                    lp_ids[i, 0] = t
-                    lp_val[i, 0] = float(lps[row])
-                    lp_rank[i] = int(handle.ranks[row])
-                row += 1
-                r.output_token_ids.append(t)
-                sampled.append([t])
-            else:
-                sampled.append([])
-        logprobs = None
-        if want_lp:
-            from vllm.v1.outputs import LogprobsLists
-
-            logprobs = LogprobsLists(lp_ids, lp_val, lp_rank)
-        return ModelRunnerOutput(req_ids=req_ids, req_id_to_index={rid: i for i, rid in enumerate(req_ids)},
-                                 sampled_token_ids=sampled, logprobs=logprobs, prompt_logprobs_dict={},
-                                 pooler_output=[])
+                r.num_pending += 1
+        result = _StepOutput(handle, req_ids, samples, want_lp)
+        if self.async_scheduling:
+            return result
+        return result.get_output()
 
     def execute_dummy_batch(self) -> None:
         """An idle data-parallel replica's step: a one-token forward on the null block (no KV
