@@ -71,3 +71,47 @@ def test_vllm_engine_through_b200_worker(tmp_path, async_sched):
     res = json.loads(lines[-1][len("RESULT"):])
     assert all(len(t) == 12 for t in res["got"])
     assert res["got"] == res["ref"]
+
+
+def test_vllm_tp2_mp_executor_gloo(tmp_path):
+    """vLLM's multiprocess executor with two B200 workers (TP = 2 over gloo on the CPU, each
+    loading its shard of one saved checkpoint) equals the framework's own single-rank engine
+    (greedy)."""
+    from tests._tiny import tiny_llama_checkpoint
+
+    ckpt, _ = tiny_llama_checkpoint()
+    script = textwrap.dedent(f"""
+        import json, os, sys
+        sys.path.insert(0, {ROOT!r})
+        import torch
+        import vllm.platforms as vp
+        from vllm_neuron_b200.vllm_plugin.platform import B200Platform
+        vp._current_platform = B200Platform()
+        from vllm import LLM, SamplingParams
+        if __name__ == "__main__":
+            g = torch.Generator().manual_seed(0)
+            prompts = [torch.randint(0, 32000, (n,), generator=g).tolist() for n in (32, 40, 7)]
+            llm = LLM(model={ckpt!r}, skip_tokenizer_init=True, dtype="float32", max_model_len=256,
+                      max_num_seqs=4, max_num_batched_tokens=64, seed=0, block_size=16,
+                      enforce_eager=True, tensor_parallel_size=2, distributed_executor_backend="mp")
+            outs = llm.generate([{{"prompt_token_ids": p}} for p in prompts],
+                                SamplingParams(max_tokens=8, temperature=0.0, ignore_eos=True))
+            got = [list(o.outputs[0].token_ids) for o in outs]
+            from vllm_neuron_b200.engine.sampling_params import SamplingParams as SP
+            from vllm_neuron_b200.entrypoints import LLM as B200LLM
+            ours = B200LLM({ckpt!r}, max_num_seqs=4, max_model_len=256, max_num_batched_tokens=64,
+                           num_gpu_blocks=128, device="cpu", dtype="float32", skip_tokenizer_init=True, seed=0)
+            ref = [list(o.outputs[0].token_ids) for o in
+                   ours.generate(prompts, SP(temperature=0.0, max_tokens=8, ignore_eos=True))]
+            print("RESULT" + json.dumps({{"got": got, "ref": ref}}), flush=True)
+    """)
+    (tmp_path / "run_tp2.py").write_text(script)
+    env = dict(os.environ, VLLM_B200_PLUGIN="1", MASTER_ADDR="127.0.0.1", VLLM_HOST_IP="127.0.0.1",
+               VLLM_WORKER_MULTIPROC_METHOD="spawn")
+    p = subprocess.run([sys.executable, str(tmp_path / "run_tp2.py")], capture_output=True, text=True,
+                       timeout=600, cwd=str(tmp_path), env=env)
+    lines = [l for l in p.stdout.splitlines() if l.startswith("RESULT")]
+    assert lines, (p.stdout[-2000:], p.stderr[-4000:])
+    res = json.loads(lines[-1][len("RESULT"):])
+    assert all(len(t) == 8 for t in res["got"])
+    assert res["got"] == res["ref"]

@@ -62,7 +62,9 @@ class B200Platform(Platform):
 
     @classmethod
     def set_device(cls, device: torch.device) -> None:
-        torch.cuda.set_device(device)
+        # a CPU worker (gloo tests) has no device to select
+        if torch.device(device).type == "cuda":
+            torch.cuda.set_device(device)
 
     @classmethod
     def inference_mode(cls):
