@@ -135,7 +135,9 @@ void gemm_w8(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, int64_t 
   }
   CHECK_BF16(act);
   const bool grouped = gtiles.has_value();
-  TORCH_CHECK(!grouped || w8 == 2 || w8 == 4, "gemm_w8: grouped mode takes the weight as B");
+  // grouped with the weight as A (w8 == 3): the swapped mode for decode-size expert batches
+  TORCH_CHECK(!grouped || w8 == 2 || w8 == 3 || w8 == 4, "gemm_w8: grouped mode takes block-FP8 weights as B");
+  const bool grouped_t = grouped && w8 == 3;
   TORCH_CHECK(a.stride(-1) == 1 && b.stride(-1) == 1 && out.stride(-1) == 1,
               "gemm_w8: inner dims must be contiguous");
   const bool f32_out = (epi == b200::EPI_F32_RED || epi == b200::EPI_F32_RED_T);
@@ -151,7 +153,18 @@ void gemm_w8(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, int64_t 
   g.M = (int)a.size(0);
   g.K = (int)act.size(-1);  // logical elements (an MXFP4 row holds K / 2 bytes)
   TORCH_CHECK(wt.size(-1) * (fp4 ? 2 : 1) == g.K, "gemm_w8: weight and activation K differ");
-  if (grouped) {
+  if (grouped_t) {
+    TORCH_CHECK(a.dim() == 3 && a.is_contiguous() && b.dim() == 2, "gemm_w8: swapped grouped a [E, rows, K/2], b [R, K]");
+    TORCH_CHECK(epi == b200::EPI_BF16_T, "gemm_w8: swapped grouped mode stores out[token, col] (EPI_BF16_T)");
+    TORCH_CHECK(out.dim() == 2 && out.size(0) >= b.size(0) && out.size(1) >= a.size(1), "gemm_w8: grouped out");
+    g.M = (int)a.size(1);
+    g.N = (int)b.size(0);
+    g.gtiles = gtiles->data_ptr<int>();
+    g.gcount = gcount.value().data_ptr<int>();
+    g.gmax = (int)gtiles->size(0);
+    g.num_groups = (int)a.size(0);
+    g.grouped_t = 1;
+  } else if (grouped) {
     TORCH_CHECK(b.dim() == 3 && b.is_contiguous(), "gemm_w8: grouped b");
     TORCH_CHECK(fp4 || b.size(1) % 128 == 0, "gemm_w8: grouped block-FP8 expert rows must be multiples of 128");
     g.N = (int)b.size(1);

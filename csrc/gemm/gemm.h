@@ -53,6 +53,9 @@ struct GemmArgs {
   const int* gcount = nullptr;
   int gmax = 0;
   int num_groups = 0;
+  // Swapped grouped mode (decode-size experts): A = stacked expert weights [num_groups * M, K],
+  // B = token rows [N, K], out[token, col] (EPI_BF16_T); each entry's rows fit one BN tile.
+  int grouped_t = 0;
   const GemmSPArgs* sp = nullptr;  // sequence-parallel fusion (null: plain GEMM)
   // FP8 (e4m3) operands: A and B hold bytes, K counts elements (multiple of 16), and the
   // accumulator is multiplied by `alpha` (per-tensor scales a * b) in the epilogue.

@@ -26,6 +26,12 @@
 // into this rank's A buffer by rank r; the producer waits (bounded) on rank r's counter before
 // its first load of those rows, so the local rows are multiplied while the peers' arrive.
 //
+// Grouped mode with swapped operands (decode-size MoE experts, GemmArgs::grouped_t): A stacks
+// the experts' weights [E * M, K] and B is the expert-sorted token rows; the tile of (entry,
+// mb) multiplies weight rows [expert * M + 128 mb, ...) by the entry's token rows (at most BN)
+// and stores out[token, 128 mb + r] (EPI_BF16_T).  Few tokens per expert then cost an N = BN
+// MMA instead of a 128-row token tile, so a 4-bit weight stream stays memory-bound.
+//
 // Grouped mode (MoE experts): the A operand is the expert-sorted token rows and B stacks the
 // experts' weights [E * N, K].  A device tile list, written by the routing kernels, gives
 // per 128-row block (expert, first row, end row); the tile of (entry, nb) multiplies rows
@@ -65,7 +71,7 @@ struct GemmParams {
   void* out;
   long long ldo;
   uint32_t* status;
-  // grouped mode
+  // grouped mode: 1 = weights as B (token tiles of 128 rows), 2 = weights as A (swapped)
   int grouped;
   const int4* gtiles;  // [entries] (expert, first row, end row, unused)
   const int* gcount;   // number of valid entries
@@ -121,6 +127,11 @@ __device__ __forceinline__ TileRows tile_rows(const GemmParams& p, int mb) {
   return t;
 }
 
+// Swapped grouped mode: first weight row (A) of tile (entry mb, block nb) and its token rows.
+__device__ __forceinline__ int gt_weight_row(const GemmParams& p, int mb, int nb) {
+  return p.gtiles[mb].x * p.M + nb * kBM;
+}
+
 __device__ __forceinline__ void decode_tile(const GemmParams& p, int tile, int& mb, int& nb,
                                             int& split) {
   const int mn_tiles = p.num_m_blocks * p.num_n_blocks;
@@ -159,6 +170,15 @@ struct SegCursor {
       k1 = (int)min((long long)p.num_k_blocks, k0 + (u_end - u));
       u += k1 - k0;
       decode_tile(p, t, mb, nb, split);
+      return true;
+    }
+    if (p.grouped == 2) {  // mb = tile-list entry, nb = 128-row block of the expert's weight
+      if (tile >= *p.gcount * p.num_m_blocks) return false;
+      mb = tile / p.num_m_blocks;
+      nb = tile - mb * p.num_m_blocks;
+      k0 = 0;
+      k1 = p.num_k_blocks;
+      tile += gridDim.x;
       return true;
     }
     if (p.grouped) {
@@ -289,8 +309,8 @@ __global__ void __launch_bounds__(W8 ? 320 : 192, 1)
       const uint64_t hint_b = kWeightIsA ? policy_evict_last()   // B = activations, reused
                                          : policy_evict_first();
       uint32_t ag_ready = 0;  // ranks whose all-gathered A rows are known complete
-      auto load_a = [&](int s, int kb, int mb) {
-        const int a_row = tile_rows(p, mb).a_row;
+      auto load_a = [&](int s, int kb, int mb, int nb) {
+        const int a_row = p.grouped == 2 ? gt_weight_row(p, mb, nb) : tile_rows(p, mb).a_row;
         if (p.sp.ag_ctr != nullptr) {
           const int r0 = a_row / p.sp.ag_rows;
           const int r1 = min(min(a_row + kBM - 1, p.M - 1) / p.sp.ag_rows, p.sp.ag_world - 1);
@@ -308,10 +328,9 @@ __global__ void __launch_bounds__(W8 ? 320 : 192, 1)
         tma_load_2d(&tmA, &full_bar[s], dst, (kFP4 && kWSide == 1) ? kb * kSRow : kb * kKElems, a_row, hint_a);
       };
       auto load_b = [&](int s, int kb, int nb, int mb) {
-        const int base = p.grouped ? tile_rows(p, mb).b_base : 0;
+        const int row = p.grouped == 2 ? p.gtiles[mb].y : (p.grouped ? tile_rows(p, mb).b_base : 0) + nb * BN;
         uint8_t* dst = kWSide == 2 ? smS + s * kSBytes : smB + s * kBTileBytes;
-        tma_load_2d(&tmB, &full_bar[s], dst, (kFP4 && kWSide == 2) ? kb * kSRow : kb * kKElems,
-                    base + nb * BN, hint_b);
+        tma_load_2d(&tmB, &full_bar[s], dst, (kFP4 && kWSide == 2) ? kb * kSRow : kb * kKElems, row, hint_b);
       };
       // The grouped tile list is written by the previous kernel.
       if (p.grouped) pdl_wait();
@@ -329,7 +348,7 @@ __global__ void __launch_bounds__(W8 ? 320 : 192, 1)
       for (int i = 0; i < STAGES; ++i) {
         if (have) {
           mbar_arrive_expect_tx(&full_bar[i], kStageTx);
-          if (kWeightIsA) load_a(i, kb, mb); else load_b(i, kb, nb, mb);
+          if (kWeightIsA) load_a(i, kb, mb, nb); else load_b(i, kb, nb, mb);
           pre_mb[i] = mb;
           pre_nb[i] = nb;
           pre_kb[i] = kb;
@@ -345,7 +364,7 @@ __global__ void __launch_bounds__(W8 ? 320 : 192, 1)
 #pragma unroll
       for (int i = 0; i < STAGES; ++i) {
         if (i < npre) {
-          if (kWeightIsA) load_b(i, pre_kb[i], pre_nb[i], pre_mb[i]); else load_a(i, pre_kb[i], pre_mb[i]);
+          if (kWeightIsA) load_b(i, pre_kb[i], pre_nb[i], pre_mb[i]); else load_a(i, pre_kb[i], pre_mb[i], pre_nb[i]);
         }
       }
       // Phase 2: steady state.
@@ -357,7 +376,7 @@ __global__ void __launch_bounds__(W8 ? 320 : 192, 1)
           break;
         }
         mbar_arrive_expect_tx(&full_bar[s], kStageTx);
-        load_a(s, kb, mb);
+        load_a(s, kb, mb, nb);
         load_b(s, kb, nb, mb);
         ++it;
         if (++kb == k1) {
@@ -431,10 +450,40 @@ __global__ void __launch_bounds__(W8 ? 320 : 192, 1)
     int mb, nb, k0, k1;
     while (ok && cur.next(p, mb, nb, k0, k1)) {
       const TileRows tr = tile_rows(p, mb);
-      const int wrow0 = kWSide == 1 ? tr.a_row : tr.b_base + nb * BN;  // first weight row of the tile
+      const int wrow0 = kWSide == 1 ? (p.grouped == 2 ? gt_weight_row(p, mb, nb) : tr.a_row)
+                                    : tr.b_base + nb * BN;  // first weight row of the tile
+      // Scales are read from global memory two k-blocks ahead of their use (two register
+      // slots), so their latency overlaps the conversion of the blocks in between.
+      constexpr int kScPer = kFP4 ? kW8Rows / 32 : 1;  // scale words per lane per k-block
+      auto load_scales = [&](int kbx, uint32_t (&d)[kScPer]) {
+        if constexpr (kFP4) {
+#pragma unroll
+          for (int i = 0; i < kScPer; ++i) {
+            const int r = cw * (kW8Rows / 4) + i * 8 + (lane >> 2);
+            const int wr = min(wrow0 + r, p.wsc_rows - 1);
+            d[i] = kbx < k1 ? __ldg(p.wsc8 + (long long)wr * p.wsc_ld + kbx * 2 + ((lane & 3) >> 1)) : 0u;
+          }
+        } else {
+          // one 128 x 128 block scale per lane (rows of a tile share the 128-row block)
+          const int r = cw * (kW8Rows / 4) + (lane >> 2);
+          const int srow = min((wrow0 + r) >> 7, p.wsc_rows - 1);
+          d[0] = kbx < k1 ? __float_as_uint(__ldg(p.wsc + (kbx >> 1) + (long long)srow * p.wsc_ld)) : 0u;
+        }
+      };
+      uint32_t sc_a[kScPer], sc_b[kScPer];
+      load_scales(k0, sc_a);
+      load_scales(k0 + 1, sc_b);
       for (int kb = k0; kb < k1; ++kb, ++it) {
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
+        const bool odd = ((kb - k0) & 1) != 0;
+        uint32_t sc_cur[kScPer];
+#pragma unroll
+        for (int i = 0; i < kScPer; ++i) sc_cur[i] = odd ? sc_b[i] : sc_a[i];
+        if (odd)
+          load_scales(kb + 2, sc_b);
+        else
+          load_scales(kb + 2, sc_a);
         if (!mbar_wait_abortable(&full_bar[s], ph, kTimeoutTmaFull, p.status, abort_flag, wait_ns)) {
           ok = false;
           break;
@@ -449,8 +498,7 @@ __global__ void __launch_bounds__(W8 ? 320 : 192, 1)
             const int r = cw * (kW8Rows / 4) + i * 8 + (lane >> 2);
             const int c = lane & 3;
             const uint2 v = *reinterpret_cast<const uint2*>(src + r * kSRow + c * 8);
-            const int wr = min(wrow0 + r, p.wsc_rows - 1);
-            const uint32_t e = __ldg(p.wsc8 + (long long)wr * p.wsc_ld + kb * 2 + (c >> 1));
+            const uint32_t e = sc_cur[i];
             const float sc = __uint_as_float(e ? (e << 23) : 0x00400000u);  // 2^(e - 127)
             uint32_t h[8];
             {
@@ -475,14 +523,12 @@ __global__ void __launch_bounds__(W8 ? 320 : 192, 1)
             *reinterpret_cast<uint4*>(drow + (((2 * c + 1) ^ sw) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
           }
         } else {
-        const float* sc_col = p.wsc + (kb >> 1);  // 128-wide scale column of this 64-k block
+        const float sc = __uint_as_float(sc_cur[0]);  // the tile's 128 x 128 block scale
 #pragma unroll
         for (int i = 0; i < kW8Rows / 32; ++i) {
           const int r = cw * (kW8Rows / 4) + i * 8 + (lane >> 2);
           const int c16 = lane & 3;
           const uint4 v = *reinterpret_cast<const uint4*>(src + r * kBK + c16 * 16);
-          const int srow = min((wrow0 + r) >> 7, p.wsc_rows - 1);
-          const float sc = __ldg(sc_col + (long long)srow * p.wsc_ld);
           const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
           uint32_t o[8];
 #pragma unroll
@@ -602,7 +648,18 @@ __global__ void __launch_bounds__(W8 ? 320 : 192, 1)
               }
             }
           } else if constexpr (EPI == EPI_BF16_T) {
-            if (m < m_lim) {
+            if (p.grouped == 2) {
+              // weight row 128 nb + row of the entry's expert -> column; token rows of the entry
+              const int4 g = p.gtiles[mb];
+              const int col = nb * kBM + row;
+              if (col < p.M) {
+                __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + col;
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (g.y + c + j < g.z)
+                    o[(long long)(g.y + c + j) * p.ldo] = __float2bfloat16(__uint_as_float(r[j]));
+              }
+            } else if (m < m_lim) {
               __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + m;
 #pragma unroll
               for (int j = 0; j < 32; ++j)
@@ -754,16 +811,20 @@ void gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
   const bool grouped = a.gtiles != nullptr;
   if (grouped && (a.splits > 1 || a.splits < 0 || a.num_groups < 1 || a.gmax < 1))
     throw std::invalid_argument("gemm: grouped mode needs splits == 1, groups and a tile bound");
+  if (a.grouped_t && (!grouped || a.epi != EPI_BF16_T || a.w8 == 2 || a.w8 == 4))
+    throw std::invalid_argument("gemm: swapped grouped mode needs a tile list, EPI_BF16_T and the weight as A");
   if (a.fp8 && (grouped || a.sp != nullptr))
     throw std::invalid_argument("gemm: FP8 operands are for the dense (non-grouped, non-SP) modes");
-  const uint64_t b_rows = grouped ? (uint64_t)a.N * a.num_groups : (uint64_t)a.N;
+  const uint64_t b_rows = grouped && !a.grouped_t ? (uint64_t)a.N * a.num_groups : (uint64_t)a.N;
+  // A rows: the stacked experts' weights in the swapped grouped mode
+  const uint64_t a_rows = a.grouped_t ? (uint64_t)a.M * a.num_groups : (uint64_t)a.M;
   const bool w4 = a.w8 == 3 || a.w8 == 4;
   if (a.w8 == 1 || a.w8 == 2) {
     if (a.fp8 || a.w_scales == nullptr || a.w_scale_rows < 1 || a.w_scale_ld < (a.K + 127) / 128)
       throw std::invalid_argument("gemm: bad block-FP8 weight arguments");
     if (a.K % 16 != 0 || (a.w8 == 1 ? a.lda : a.ldb) % 16 != 0)
       throw std::invalid_argument("gemm: block-FP8 weight rows must be multiples of 16 bytes");
-    const uint64_t wrows = a.w8 == 1 ? (uint64_t)a.M : b_rows;
+    const uint64_t wrows = a.w8 == 1 ? a_rows : b_rows;
     if ((uint64_t)a.w_scale_rows < (wrows + 127) / 128)
       throw std::invalid_argument("gemm: block-FP8 scale rows do not cover the weight rows");
   } else if (w4) {
@@ -771,23 +832,23 @@ void gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
       throw std::invalid_argument("gemm: bad MXFP4 weight arguments (K must be a multiple of 64)");
     if ((a.w8 == 3 ? a.lda : a.ldb) % 16 != 0)
       throw std::invalid_argument("gemm: MXFP4 weight rows must be multiples of 16 bytes");
-    const uint64_t wrows = a.w8 == 3 ? (uint64_t)a.M : b_rows;
+    const uint64_t wrows = a.w8 == 3 ? a_rows : b_rows;
     if ((uint64_t)a.w_scale_rows < wrows)
       throw std::invalid_argument("gemm: MXFP4 scale rows do not cover the weight rows");
   } else if (a.w8 != 0) {
     throw std::invalid_argument("gemm: w8 must be 0..4");
   }
   // block-FP8 weight operand: bytes, 64 per row per stage, no swizzle (the converter swizzles)
-  const CUtensorMap ta = a.w8 == 3 ? make_tmap_u8_2d(a.A, a.K / 2, a.M, a.lda, kBK / 2, kBM, 0)
-                         : a.w8 == 1 ? make_tmap_u8_2d(a.A, a.K, a.M, a.lda, kBK, kBM, 0)
-                         : a.fp8   ? make_tmap_u8_2d(a.A, a.K, a.M, a.lda, 128, kBM, 128)
-                                   : make_tmap_bf16_2d(a.A, a.K, a.M, a.lda, kBK, kBM, true);
+  const CUtensorMap ta = a.w8 == 3 ? make_tmap_u8_2d(a.A, a.K / 2, a_rows, a.lda, kBK / 2, kBM, 0)
+                         : a.w8 == 1 ? make_tmap_u8_2d(a.A, a.K, a_rows, a.lda, kBK, kBM, 0)
+                         : a.fp8   ? make_tmap_u8_2d(a.A, a.K, a_rows, a.lda, 128, kBM, 128)
+                                   : make_tmap_bf16_2d(a.A, a.K, a_rows, a.lda, kBK, kBM, true);
   const CUtensorMap tb = a.w8 == 4 ? make_tmap_u8_2d(a.B, a.K / 2, b_rows, a.ldb, kBK / 2, bn, 0)
                          : a.w8 == 2 ? make_tmap_u8_2d(a.B, a.K, b_rows, a.ldb, kBK, bn, 0)
                          : a.fp8   ? make_tmap_u8_2d(a.B, a.K, b_rows, a.ldb, 128, bn, 128)
                                    : make_tmap_bf16_2d(a.B, a.K, b_rows, a.ldb, kBK, bn, true);
   GemmParams p;
-  p.grouped = grouped ? 1 : 0;
+  p.grouped = grouped ? (a.grouped_t ? 2 : 1) : 0;
   p.gtiles = reinterpret_cast<const int4*>(a.gtiles);
   p.gcount = a.gcount;
   p.M = a.M;
@@ -824,7 +885,9 @@ void gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
   p.out = a.out;
   p.ldo = a.ldo;
   p.status = a.status;
-  const long long tiles = grouped ? (long long)a.gmax * p.num_n_blocks
+  if (a.grouped_t) p.num_n_blocks = 1;  // an entry's tokens fit one BN tile
+  const long long tiles = a.grouped_t ? (long long)a.gmax * p.num_m_blocks
+                          : grouped ? (long long)a.gmax * p.num_n_blocks
                                   : (long long)p.num_m_blocks * p.num_n_blocks * p.splits;
   int grid = num_sms_cached();
   if (a.max_ctas > 0 && a.max_ctas < grid) grid = a.max_ctas;
@@ -880,6 +943,9 @@ void gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
     B200_GEMM_W8_CASE(3, 32, 8, EPI_F32_RED_T)
     B200_GEMM_W8_CASE(3, 64, 7, EPI_F32_RED_T)
     B200_GEMM_W8_CASE(3, 128, 5, EPI_F32_RED_T)
+    B200_GEMM_W8_CASE(3, 16, 8, EPI_BF16_T)
+    B200_GEMM_W8_CASE(3, 32, 8, EPI_BF16_T)
+    B200_GEMM_W8_CASE(3, 64, 7, EPI_BF16_T)
     B200_GEMM_W8_CASE(4, 256, 3, EPI_BF16)
     B200_GEMM_W8_CASE(4, 128, 5, EPI_BF16)
     throw std::invalid_argument("gemm (fp8 / fp4 weight): unsupported (operand, bn, epilogue): w8=" +

@@ -75,3 +75,32 @@ def test_mxfp4_moe_block_gptoss(cuda_device, T):
                       router_b=rb.cpu(), b_gu=b_gu.cpu(), b_down=b_dn.cpu(), act=M.ACT_GPTOSS,
                       alpha=1.702, limit=7.0)
     assert _rel(out.cpu(), ref) < 3e-2
+
+
+@pytest.mark.parametrize("N,K,bn", [(5760, 2880, 16), (2880, 2880, 64), (1024, 512, 32)])
+def test_mxfp4_grouped_swapped(cuda_device, N, K, bn):
+    """Decode-size experts: weights as the 128-row operand, each expert's <= bn tokens as the N
+    tile, transposed store (the swapped grouped mode of the tcgen05 GEMM)."""
+    E = 6
+    w = _mx(E, N, K, cuda_device, seed=N + bn)
+    counts = [min(bn, c) for c in (1, 0, bn, 3, bn - 1, 2)]  # expert 1 has no tokens
+    rows = sum(counts)
+    x = (torch.randn(rows, K, device=cuda_device) * 0.5).to(torch.bfloat16)
+    tiles, r = [], 0
+    for e, c in enumerate(counts):
+        if c:
+            tiles.append([e, r, r + c, 0])
+        r += c
+    gt = torch.tensor(tiles + [[0, 0, 0, 0]] * 3, dtype=torch.int32, device=cuda_device)  # spare entries
+    cnt = torch.tensor([len(tiles)], dtype=torch.int32, device=cuda_device)
+    out = torch.full((rows, N), float("nan"), dtype=torch.bfloat16, device=cuda_device)
+    ext().gemm_w8(w.q, x, out, L.EPI_BF16_T, bn, 1, w.scales, 3, gt, cnt)
+    torch.cuda.synchronize()
+    wd = w.dequant().float()
+    r = 0
+    for e, c in enumerate(counts):
+        if c:
+            ref = x[r:r + c].float() @ wd[e].t()
+            assert _rel(out[r:r + c], ref) < 1e-2, e
+        r += c
+    assert not torch.isnan(out).any()

@@ -37,6 +37,9 @@ ROUTE_SIGMOID_BIAS_TOPK = 3  # rank by sigmoid + correction bias, weigh by the p
 ACT_SILU = 0
 ACT_GPTOSS = 1
 EPI_BF16 = 0
+EPI_BF16_T = 1
+# decode-size expert batches (at most this many tokens) run the swapped grouped GEMM
+SWAP_MAX_TOKENS = 64
 
 
 @dataclass
@@ -317,10 +320,17 @@ def _experts_cuda(x, ids, w, w_gu, w_down, k, b_gu, b_down, act, alpha, limit, e
     ext().moe_gather(x, ws.sorted_src, k, ws.offsets, xp)
     gu = ws.gu[:R]
     use_fp4 = fp4_gu is not None and T <= fp4_max_tokens
+    # decode-size MXFP4 batches: swapped grouped tcgen05 GEMM (expert weight rows as the 128-row
+    # operand, the <= 64 tokens of each expert as an N tile), so the 4-bit stream stays
+    # memory-bound; an expert holds at most T rows, so each tile-list entry fits one N tile
+    swap_fp4 = not use_fp4 and isinstance(w_gu, L.MXFP4Weight) and T <= SWAP_MAX_TOKENS
+    bn_t = L.skinny_bn(T) if swap_fp4 else 0
     # every tile-list entry holds >= 1 row: at most R entries exist (bounds the fp4 grid)
     gt = ws.gtiles[:min(ws.gtiles.shape[0], R)]
     if use_fp4:
         ext().moe_mxfp4_gemm(xp, fp4_gu, gu, gt, ws.gcount)
+    elif swap_fp4:
+        ext().gemm_w8(w_gu.q, xp, gu, EPI_BF16_T, bn_t, 1, w_gu.scales, 3, gt, ws.gcount)
     elif isinstance(w_gu, L.BlockFP8Weight):
         ext().gemm_w8(xp, w_gu.q, gu, EPI_BF16, 256, 1, w_gu.scales, 2, ws.gtiles, ws.gcount)
     elif isinstance(w_gu, L.MXFP4Weight):
@@ -333,6 +343,8 @@ def _experts_cuda(x, ids, w, w_gu, w_down, k, b_gu, b_down, act, alpha, limit, e
     bn_down = 256 if H % 256 == 0 else 128
     if use_fp4:
         ext().moe_mxfp4_gemm(a, fp4_down, y, gt, ws.gcount)
+    elif swap_fp4 and isinstance(w_down, L.MXFP4Weight):
+        ext().gemm_w8(w_down.q, a, y, EPI_BF16_T, bn_t, 1, w_down.scales, 3, gt, ws.gcount)
     elif isinstance(w_down, L.BlockFP8Weight):
         ext().gemm_w8(a, w_down.q, y, EPI_BF16, bn_down, 1, w_down.scales, 2, ws.gtiles, ws.gcount)
     elif isinstance(w_down, L.MXFP4Weight):
