@@ -437,9 +437,22 @@ void gemm2sm_set(bool on) { g_2sm_on.store(on ? 1 : 0, std::memory_order_relaxed
 int gemm2sm_pairs() { return max_pairs(); }
 
 bool gemm2sm_eligible(const GemmArgs& a) {
-  return gemm2sm_enabled() && a.fp8 == 0 && a.w8 == 0 && a.gtiles == nullptr && a.sp == nullptr &&
-         (a.epi == EPI_BF16 || (a.epi == EPI_SILU_BF16 && a.N % kTile == 0)) && a.splits <= 1 &&
-         a.splits >= 0 && a.M >= 2 * kTile && a.K % 8 == 0 && a.lda % 8 == 0 && a.ldb % 8 == 0;
+  if (!(gemm2sm_enabled() && a.fp8 == 0 && a.w8 == 0 && a.gtiles == nullptr && a.sp == nullptr &&
+        (a.epi == EPI_BF16 || (a.epi == EPI_SILU_BF16 && a.N % kTile == 0)) && a.splits <= 1 &&
+        a.splits >= 0 && a.M >= 2 * kTile && a.K % 8 == 0 && a.lda % 8 == 0 && a.ldb % 8 == 0))
+    return false;
+  // Wave quantization: the pair kernel is ~1.15x faster per tile-wave on the large shapes, but
+  // its 256 x 256 tiles come in fewer, coarser waves (a TP-sharded qkv of 768 columns has 96
+  // tiles for 74 pairs).  Keep the single-SM kernel (128 x bn tiles) when its waves are fuller
+  // by more than that margin.
+  const int sms = num_sms_cached();
+  const int pairs = max(1, sms / 2);
+  const int bn1 = a.bn > 0 ? a.bn : 256;
+  const long long t2 = (long long)((a.M + kTile - 1) / kTile) * ((a.N + kTile - 1) / kTile);
+  const long long t1 = (long long)((a.M + 127) / 128) * ((a.N + bn1 - 1) / bn1);
+  const double eff2 = (double)t2 / (double)(((t2 + pairs - 1) / pairs) * pairs);
+  const double eff1 = (double)t1 / (double)(((t1 + sms - 1) / sms) * sms);
+  return eff2 * 1.15 >= eff1;
 }
 
 void gemm2sm_launch(const GemmArgs& a, cudaStream_t stream) {
