@@ -231,7 +231,9 @@ def build_runner(args: EngineArgs, model, max_model_len: int, device, b200_confi
                        block_size=args.block_size * max(1, args.decode_context_parallel_size),
                        cuda_graphs=(args.cuda_graphs and b200_config.cuda_graphs
                                     and getattr(model, "supports_cuda_graphs", True)),
-                       device=device, seed=args.seed)
+                       device=device, seed=args.seed,
+                       # the reference's decode batch buckets select the captured decode graphs
+                       graph_buckets=b200_config.num_seqs_buckets)
 
 
 class LLMEngine:

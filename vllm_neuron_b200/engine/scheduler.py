@@ -15,10 +15,10 @@ behaviour for API parity.  Bucket padding statistics for ``num_batched_tokens_bu
 """
 from __future__ import annotations
 
-import bisect
 from collections import deque
 from dataclasses import dataclass, field
 
+from ..utils.buckets import bucket_for  # noqa: F401 (re-exported)
 from .block_manager import BlockManager
 from .request import Request, RequestStatus
 
@@ -54,13 +54,6 @@ class SchedulerOutput:
     @property
     def empty(self) -> bool:
         return not self.scheduled
-
-
-def bucket_for(buckets: list[int] | None, n: int) -> int:
-    if not buckets:
-        return n
-    i = bisect.bisect_left(buckets, n)
-    return buckets[i] if i < len(buckets) else n
 
 
 class Scheduler:

@@ -86,11 +86,10 @@ class ModelRunner:
         self.dcp_size, self.dcp_rank, self.cache_block_size = 1, 0, block_size
         self.use_graphs = cuda_graphs and self.is_cuda and not envs.VLLM_B200_DISABLE_CUDA_GRAPHS
         self._last_prefill_rows = ops.attention.PREFILL_ROWS  # rows per prefill work item
+        from ..utils.buckets import decode_graph_buckets
+
         cap = min(max_num_seqs, model.max_decode_tokens)
-        self.graph_buckets = sorted(b for b in (graph_buckets or [1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128])
-                                    if b <= cap)
-        if cap not in self.graph_buckets and cap > 0:
-            self.graph_buckets.append(cap)
+        self.graph_buckets = decode_graph_buckets(cap, graph_buckets)
         self.graphs: dict[int, tuple] = {}
         self.seed = seed
         self.num_sms = torch.cuda.get_device_properties(self.device).multi_processor_count if self.is_cuda else 148
