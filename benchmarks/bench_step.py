@@ -28,6 +28,38 @@ from vllm_neuron_b200.engine.scheduler import ScheduledRequest, SchedulerOutput 
 from vllm_neuron_b200.entrypoints import LLM  # noqa: E402
 
 
+def decode_timeline(replay, n: int) -> list[dict]:
+    """Per-kernel share of ``n`` replays of a decode graph: kernels sorted by start; each one's
+    increment is how far its end moves the running maximum end time (launches that overlap under
+    programmatic dependent launch are charged only for what they add to the step)."""
+    import re
+    from collections import OrderedDict
+
+    from torch.profiler import ProfilerActivity, profile
+
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(n):
+            replay()
+        torch.cuda.synchronize()
+    ev = sorted((e.time_range.start, e.time_range.end, e.name) for e in prof.events()
+                if e.device_type == torch.autograd.DeviceType.CUDA)
+    if not ev:
+        return []
+    agg: OrderedDict[str, list] = OrderedDict()
+    last = ev[0][0]
+    for s0, e1, name in ev:
+        inc = max(0.0, e1 - last)
+        last = max(last, e1)
+        key = re.sub(r"\(.*", "", name)[:80]
+        a = agg.setdefault(key, [0, 0.0])
+        a[0] += 1
+        a[1] += inc
+    total = sum(v[1] for v in agg.values()) or 1.0
+    return [{"kernel": k, "launches_per_step": c / n, "us_per_step": t / n, "share": t / total}
+            for k, (c, t) in sorted(agg.items(), key=lambda kv: -kv[1][1])]
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--model", default="llama3-8b", choices=sorted(MODELS))
@@ -41,6 +73,10 @@ def main():
     ap.add_argument("--sp", action="store_true", help="TP prefill: sequence parallelism (fused unless --no-fused)")
     ap.add_argument("--emulate-tp", type=int, default=1,
                     help="one GPU runs rank 0's share of TP=N with local no-op collectives (profiling only)")
+    ap.add_argument("--timeline", action="store_true",
+                    help="break the decode step's graph replay into per-kernel increments (torch "
+                         "profiler trace of 10 replays; a kernel's increment is how far it moves the "
+                         "last kernel end, so PDL overlap is not double-counted)")
     ap.add_argument("--profile-once", action="store_true",
                     help="run one decode replay and one prefill chunk inside NVTX ranges "
                          "'decode_step' / 'prefill_chunk' (for an ncu launch list)")
@@ -131,6 +167,8 @@ def main():
     torch.cuda.synchronize()
     res["decode_step_gpu_ms"] = e0.elapsed_time(e1) / a.iters
     res["attn_splits"] = splits
+    if a.timeline:
+        res["decode_timeline"] = decode_timeline(g.replay, 10)
     t0 = time.perf_counter()
     for _ in range(200):
         runner._pack(out, lay, pad_B=min(b for b in runner.graphs if b >= B))
