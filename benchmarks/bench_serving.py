@@ -82,6 +82,8 @@ def main():
                          "fp8_block: 128 x 128 block-scaled FP8 weights, bf16 activations; auto: the "
                          "configuration's own (fp8_block for llama3-70b and qwen3.6-a3b)")
     ap.add_argument("--sp", action="store_true", help="sequence-parallel prefill (TP > 1)")
+    ap.add_argument("--fp8-block-act", choices=["fp8", "bf16"], default=None,
+                    help="block-FP8 decode projections: W8A8 (fp8 activations) or W8A16")
     ap.add_argument("--baseline", action="store_true",
                     help="NCCL + cuBLAS build of the same engine (no fused kernels, library GEMMs)")
     a = ap.parse_args()
@@ -108,6 +110,8 @@ def main():
         nc["sequence_parallel"] = True
     if a.baseline:
         nc.update(fused_comm=False, use_cublas_baseline=True)
+    if a.fp8_block_act:
+        nc["fp8_block_activations"] = a.fp8_block_act
     mnbt = a.max_num_batched_tokens or m.get("mnbt", 8192)
     llm = LLM(dict(m["cfg"]), tensor_parallel_size=world, max_num_seqs=P, max_model_len=max_len,
               max_num_batched_tokens=mnbt, load_format="dummy", num_gpu_blocks=blocks,
@@ -141,7 +145,9 @@ def main():
            "output_tok_s": P * OUT / (ms / 1e3), "wall_s": wall, "device_s": ms / 1e3,
            "p50_ttft_ms": float(np.median(ttft)) * 1e3, "p50_tpot_ms": float(np.median(tpot)) * 1e3,
            "dtype": "bf16" + ({"fp8_static": " activations, fp8 W8A8 projections",
-                               "fp8_block": " activations, 128x128 block-scaled fp8 weights"}.get(quant, "")),
+                               "fp8_block": (" activations, 128x128 block-scaled fp8 weights (decode: "
+                                             + ("W8A16" if a.fp8_block_act == "bf16" else
+                                                "W8A8, 1x128 fp8 activation blocks") + ")")}.get(quant, "")),
            "sp": bool(nc.get("sequence_parallel")), "max_num_batched_tokens": mnbt,
            "build": "nccl+cublas baseline" if a.baseline else "fused sm_100a",
            "data": "synthetic prompts, random-init weights"}

@@ -196,6 +196,65 @@ void gemm_w8(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, int64_t 
   check_launch("gemm_w8");
 }
 
+// Per-token, per-128-column FP8 quantization: out (e4m3) and scales [rows, cols / 128] fp32.
+void quant_fp8_block(const at::Tensor& x, at::Tensor& out, at::Tensor& scales) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  TORCH_CHECK(out.scalar_type() == at::kFloat8_e4m3fn && scales.scalar_type() == at::kFloat,
+              "quant_fp8_block: out e4m3, scales fp32");
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && out.stride(1) == 1 && scales.stride(1) == 1,
+              "quant_fp8_block: contiguous rows");
+  TORCH_CHECK(out.size(0) >= x.size(0) && scales.size(0) >= x.size(0) && scales.size(1) >= x.size(1) / 128,
+              "quant_fp8_block: output shapes");
+  const c10::cuda::CUDAGuard guard(x.device());
+  b200::quant_fp8_block_launch(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0),
+                               reinterpret_cast<uint8_t*>(out.data_ptr()), out.stride(0),
+                               scales.data_ptr<float>(), (int)scales.stride(0), (int)x.size(0),
+                               (int)x.size(1), cur_stream());
+  check_launch("quant_fp8_block");
+}
+
+// Block-scaled FP8 W8A8 decode GEMM: out[n, m] += sum_k w[m, k] xq[n, k] * ws[m / 128, k / 128] *
+// xs[n, k / 128] (fp32 reductions, weights as the 128-row operand; per-k-block promotion).
+void gemm_fp8_block(const at::Tensor& w, const at::Tensor& xq, at::Tensor& out, int64_t bn, int64_t splits,
+                    const at::Tensor& w_scales, const at::Tensor& x_scales) {
+  CHECK_CUDA(w);
+  CHECK_CUDA(xq);
+  TORCH_CHECK(w.scalar_type() == at::kFloat8_e4m3fn && xq.scalar_type() == at::kFloat8_e4m3fn,
+              "gemm_fp8_block: operands must be float8_e4m3fn");
+  TORCH_CHECK(w.dim() == 2 && xq.dim() == 2 && w.size(1) == xq.size(1), "gemm_fp8_block: bad shapes");
+  TORCH_CHECK(w.stride(1) == 1 && xq.stride(1) == 1 && out.stride(1) == 1, "gemm_fp8_block: inner dims");
+  TORCH_CHECK(out.scalar_type() == at::kFloat, "gemm_fp8_block: out must be fp32 (reductions)");
+  TORCH_CHECK(w_scales.scalar_type() == at::kFloat && x_scales.scalar_type() == at::kFloat &&
+                  w_scales.stride(1) == 1 && x_scales.stride(1) == 1,
+              "gemm_fp8_block: scales must be fp32 with contiguous rows");
+  const c10::cuda::CUDAGuard guard(w.device());
+  b200::GemmArgs g{};
+  g.A = w.data_ptr();
+  g.B = xq.data_ptr();
+  g.out = out.data_ptr();
+  g.lda = w.stride(0);
+  g.ldb = xq.stride(0);
+  g.ldo = out.stride(0);
+  g.M = (int)w.size(0);
+  g.N = (int)xq.size(0);
+  g.K = (int)w.size(1);
+  g.bn = (int)bn;
+  g.epi = b200::EPI_F32_RED_T;
+  g.splits = (int)splits;
+  g.status = status_word();
+  g.fp8 = 1;
+  g.w8 = 5;
+  g.w_scales = w_scales.data_ptr<float>();
+  g.w_scale_ld = (int)w_scales.stride(0);
+  g.w_scale_rows = (int)w_scales.size(0);
+  g.x_scales = x_scales.data_ptr<float>();
+  g.x_scale_ld = (int)x_scales.stride(0);
+  if (g.M == 0 || g.N == 0) return;
+  b200::gemm_bf16_launch(g, cur_stream());
+  check_launch("gemm_fp8_block");
+}
+
 // FP8 (e4m3) GEMM with per-tensor scales: out = alpha * (a @ b^T) (epilogue as in `gemm`).
 void gemm_fp8(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, int64_t epi, int64_t bn,
               int64_t splits, double alpha) {
@@ -1087,6 +1146,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_2sm_pairs", []() { return b200::gemm2sm_pairs(); });
   m.def("gemm_sp", &gemm_sp);
   m.def("gemm_fp8", &gemm_fp8);
+  m.def("gemm_fp8_block", &gemm_fp8_block);
+  m.def("quant_fp8_block", &quant_fp8_block);
   m.def("quant_fp8", &quant_fp8);
   m.def("rmsnorm_quant", &rmsnorm_quant);
   m.def("sp_norm_push", &sp_norm_push);

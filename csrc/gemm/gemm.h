@@ -72,6 +72,12 @@ struct GemmArgs {
   // (lower k in the low nibble), rows of K / 2 bytes (lda / ldb in bytes), with one e8m0 scale
   // byte per 32 elements: w_scales8 [w_scale_rows][w_scale_ld] (one row per weight row).
   const uint8_t* w_scales8 = nullptr;
+  // Block-scaled FP8 W8A8 (w8 = 5, fp8 = 1, EPI_F32_RED_T, weights as A): w_scales are the
+  // weight's fp32 128 x 128 block scales, x_scales [N tokens][x_scale_ld] the activations' fp32
+  // scales per token and 128-wide k block; each k block is summed with its scales applied
+  // (per-k-block promotion), so no operand is widened.
+  const float* x_scales = nullptr;
+  int x_scale_ld = 0;
 };
 
 void gemm_bf16_launch(const GemmArgs& args, cudaStream_t stream);

@@ -39,6 +39,14 @@
 // entry's end row only.  Rows past the end of the block belong to the next expert (or are
 // TMA zero fill) and are discarded.
 //
+// Block-scaled FP8 W8A8 with per-k-block promotion (W8 = 5, FP8 operands, swapped decode
+// layout EPI_F32_RED_T): e4m3 weights with one fp32 scale per 128 x 128 block and e4m3
+// activations with one fp32 scale per token and 128-wide k block.  Each stage is one 128-wide k
+// block; its MMAs go into a fresh TMEM accumulator (two alternate), and the epilogue warps add
+// it into fp32 registers scaled by the tile's weight-block scale times each token's activation
+// scale, then reduce the tile's sum into the output once.  No weight conversion: the fp8 bytes
+// stream from HBM straight into the tensor cores.
+//
 // FP8 (e4m3 x e4m3, per-tensor scales): tcgen05.mma kind::f8f6f4 on the same byte tiles, 128
 // elements per k-block, the accumulator scaled by alpha = scale_a * scale_b in the epilogue
 // (static W8A8 checkpoints: the reference's ModelOpt FP8 Llama, model/llama3/quantization.py).
@@ -82,6 +90,8 @@ struct GemmParams {
   const float* wsc;
   int wsc_ld, wsc_rows;
   const uint8_t* wsc8;  // MXFP4: e8m0 scale bytes [wsc_rows][wsc_ld], one per 32 elements
+  const float* xsc;     // W8 = 5: activation scales [tokens][xsc_ld], one per 128-wide k block
+  int xsc_ld;
 };
 
 // Bounded wait until a monotonic counter (written by a peer with a system-scope release)
@@ -235,12 +245,16 @@ __device__ __forceinline__ void fp4x8_to_f16x8_gemm(uint32_t w, uint32_t (&o)[4]
 // per stage (two e2m1 per byte), widened with the hardware e2m1x2 conversion and the e8m0
 // scale of each 32-element block -- half a byte per element from HBM.
 template <int BN, int STAGES, int EPI, bool FP8 = false, int W8 = 0>
-__global__ void __launch_bounds__(W8 ? 320 : 192, 1)
+__global__ void __launch_bounds__((W8 >= 1 && W8 <= 4) ? 320 : 192, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA,
                      const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
   constexpr int kBTileBytes = BN * kBK * 2;
-  constexpr bool kFP4 = W8 >= 3;                             // MXFP4 (else block FP8)
-  constexpr int kWSide = W8 == 0 ? 0 : (W8 == 1 || W8 == 3) ? 1 : 2;  // weight operand: A / B
+  constexpr bool kConv = W8 >= 1 && W8 <= 4;                 // converter warps widen the weight
+  constexpr bool kPromote = W8 == 5;                         // block-scaled FP8, per-k-block sums
+  static_assert(!kPromote || (FP8 && EPI == EPI_F32_RED_T && BN <= 64),
+                "promotion mode: FP8 operands, swapped decode layout, N tile <= 64");
+  constexpr bool kFP4 = W8 == 3 || W8 == 4;                  // MXFP4 (else block FP8)
+  constexpr int kWSide = !kConv ? 0 : (W8 == 1 || W8 == 3) ? 1 : 2;  // weight operand: A / B
   constexpr int kW8Rows = kWSide == 1 ? kBM : kWSide == 2 ? BN : 0;  // weight rows per tile
   constexpr int kSRow = kFP4 ? kBK / 2 : kBK;                 // staged bytes per row per stage
   constexpr int kSBytes = kW8Rows * kSRow;                    // staging bytes per stage
@@ -402,19 +416,31 @@ __global__ void __launch_bounds__(W8 ? 320 : 192, 1)
       bool ok = true;
       SegCursor cur(p);
       int mb, nb, k0, k1;
+      uint32_t u = 0;  // promotion mode: k blocks issued (accumulator = u & 1)
       for (; ok && cur.next(p, mb, nb, k0, k1); ++t_local) {
         const int acc = t_local & 1;
         const uint32_t aph = (t_local >> 1) & 1;
-        if (!mbar_wait_abortable(&tempty_bar[acc], aph ^ 1, kTimeoutTmemEmpty, p.status, abort_flag, wait_ns)) {
+        if (!kPromote &&
+            !mbar_wait_abortable(&tempty_bar[acc], aph ^ 1, kTimeoutTmemEmpty, p.status, abort_flag, wait_ns)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * BN;
+        uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = k0; kb < k1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
-          if (!mbar_wait_abortable(W8 ? &conv_bar[s] : &full_bar[s], ph, kTimeoutTmaFull, p.status,
+          if constexpr (kPromote) {
+            // each k block into its own accumulator, once the epilogue has drained it
+            const int pa = u & 1;
+            if (!mbar_wait_abortable(&tempty_bar[pa], ((u >> 1) & 1) ^ 1, kTimeoutTmemEmpty, p.status,
+                                     abort_flag, wait_ns)) {
+              ok = false;
+              break;
+            }
+            d_tmem = tmem_base + pa * BN;
+          }
+          if (!mbar_wait_abortable(kConv ? &conv_bar[s] : &full_bar[s], ph, kTimeoutTmaFull, p.status,
                                    abort_flag, wait_ns)) {
             ok = false;
             break;
@@ -426,17 +452,22 @@ __global__ void __launch_bounds__(W8 ? 320 : 192, 1)
           for (int k = 0; k < kBK / 16; ++k) {
             const uint64_t adesc = make_sdesc_sw128(a_addr + k * 32);
             const uint64_t bdesc = make_sdesc_sw128(b_addr + k * 32);
+            const uint32_t accum = kPromote ? (k > 0 ? 1u : 0u) : ((kb > k0 || k > 0) ? 1u : 0u);
             if constexpr (FP8)
-              umma_f8_ss(d_tmem, adesc, bdesc, kIdesc, (kb > k0 || k > 0) ? 1u : 0u);
+              umma_f8_ss(d_tmem, adesc, bdesc, kIdesc, accum);
             else
-              umma_f16_ss(d_tmem, adesc, bdesc, kIdesc, (kb > k0 || k > 0) ? 1u : 0u);
+              umma_f16_ss(d_tmem, adesc, bdesc, kIdesc, accum);
           }
           umma_commit(&empty_bar[s]);
+          if constexpr (kPromote) {
+            umma_commit(&tfull_bar[u & 1]);
+            ++u;
+          }
         }
-        if (ok) umma_commit(&tfull_bar[acc]);
+        if (ok && !kPromote) umma_commit(&tfull_bar[acc]);
       }
     }
-  } else if (W8 != 0 && warp >= 6) {
+  } else if (kConv && warp >= 6) {
     // ------------------------------ fp8 -> bf16 weight converter ------------------------------
     // Lane l of converter warp cw reads 16 staged bytes (row r, bytes 16 * (l % 4) ..) and
     // writes them as 16 bf16 = 16-byte chunks 2 (l % 4) and 2 (l % 4) + 1 of the 128-byte
@@ -559,6 +590,53 @@ __global__ void __launch_bounds__(W8 ? 320 : 192, 1)
     int t_local = 0;
     SegCursor cur(p);
     int mb, nb, k0, k1;
+    if constexpr (kPromote) {
+      // per k block: read its accumulator, scale by the weight block's scale times each token's
+      // activation scale, add into registers; reduce the tile's sum into out[n, m] once
+      uint32_t u = 0;
+      bool ok = true;
+      while (ok && cur.next(p, mb, nb, k0, k1)) {
+        const TileRows trows = tile_rows(p, mb);
+        const int m = trows.a_row + row;  // weight row = output column
+        const int n_base = nb * BN;       // first token of the tile
+        const float* wsc_row = p.wsc + (long long)min(trows.a_row >> 7, p.wsc_rows - 1) * p.wsc_ld;
+        float racc[BN];
+#pragma unroll
+        for (int j = 0; j < BN; ++j) racc[j] = 0.f;
+        for (int kb = k0; kb < k1; ++kb, ++u) {
+          const int pa = u & 1;
+          if (!mbar_wait_abortable(&tfull_bar[pa], (u >> 1) & 1, kTimeoutTmemFull, p.status, abort_flag, wait_ns)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const float sw = __ldg(wsc_row + kb);
+          const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + pa * BN;
+#pragma unroll
+          for (int c = 0; c < BN; c += 16) {
+            uint32_t r[16];
+            tmem_ld_32x32b_x16(t_row + c, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int n = n_base + c + j;
+              const float sx = n < p.N ? __ldg(p.xsc + (long long)n * p.xsc_ld + kb) : 0.f;
+              racc[c + j] = fmaf(__uint_as_float(r[j]), sw * sx, racc[c + j]);
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty_bar[pa]);
+        }
+        if (!ok) break;
+        if (m < trows.m_lim) {
+          float* o = reinterpret_cast<float*>(p.out) + m;
+#pragma unroll
+          for (int j = 0; j < BN; ++j)
+            if (n_base + j < p.N) atomicAdd(o + (long long)(n_base + j) * p.ldo, racc[j]);
+        }
+      }
+    } else
     for (; cur.next(p, mb, nb, k0, k1); ++t_local) {
       const int acc = t_local & 1;
       const uint32_t aph = (t_local >> 1) & 1;
@@ -778,13 +856,13 @@ template <int BN, int STAGES, int EPI, bool FP8 = false, int W8 = 0>
 static void launch_impl(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
                         int grid, cudaStream_t stream) {
   constexpr int w8_rows = (W8 == 1 || W8 == 3) ? kBM : (W8 == 2 || W8 == 4) ? BN : 0;
-  constexpr int srow = W8 >= 3 ? kBK / 2 : kBK;
+  constexpr int srow = (W8 == 3 || W8 == 4) ? kBK / 2 : kBK;
   constexpr int smem = STAGES * (kATileBytes + BN * kBK * 2 + w8_rows * srow) + 1024 + 256;
   static_assert(smem <= 232448, "shared memory budget");
   auto kern = gemm_bf16_kernel<BN, STAGES, EPI, FP8, W8>;
   static std::atomic<uint64_t> configured{0};  // per instantiation, per device
   set_max_dynamic_smem_once(kern, smem, configured);
-  launch_pdl(kern, dim3(grid), dim3(W8 ? 320 : 192), smem, stream, ta, tb, p);
+  launch_pdl(kern, dim3(grid), dim3((W8 >= 1 && W8 <= 4) ? 320 : 192), smem, stream, ta, tb, p);
 }
 
 int num_sms_cached() {
@@ -835,8 +913,14 @@ void gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
     const uint64_t wrows = a.w8 == 3 ? a_rows : b_rows;
     if ((uint64_t)a.w_scale_rows < wrows)
       throw std::invalid_argument("gemm: MXFP4 scale rows do not cover the weight rows");
+  } else if (a.w8 == 5) {
+    if (!a.fp8 || a.w_scales == nullptr || a.x_scales == nullptr || a.epi != EPI_F32_RED_T || grouped ||
+        a.sp != nullptr || a.K % 128 != 0 || a.M % 128 != 0 || a.w_scale_ld < a.K / 128 ||
+        a.x_scale_ld < a.K / 128 || (uint64_t)a.w_scale_rows < (uint64_t)a.M / 128)
+      throw std::invalid_argument("gemm: block-scaled FP8 W8A8 needs e4m3 operands, weight (A) and "
+                                  "activation (B) block scales, EPI_F32_RED_T, K and weight rows in 128s");
   } else if (a.w8 != 0) {
-    throw std::invalid_argument("gemm: w8 must be 0..4");
+    throw std::invalid_argument("gemm: w8 must be 0..5");
   }
   // block-FP8 weight operand: bytes, 64 per row per stage, no swizzle (the converter swizzles)
   const CUtensorMap ta = a.w8 == 3 ? make_tmap_u8_2d(a.A, a.K / 2, a_rows, a.lda, kBK / 2, kBM, 0)
@@ -863,6 +947,8 @@ void gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
   p.wsc_ld = a.w_scale_ld;
   p.wsc_rows = a.w_scale_rows;
   p.wsc8 = a.w_scales8;
+  p.xsc = a.x_scales;
+  p.xsc_ld = a.x_scale_ld;
   p.streamk = a.splits < 0 ? 1 : 0;
   int splits = a.splits < 1 ? 1 : a.splits;
   if (splits > p.num_k_blocks) splits = p.num_k_blocks;
@@ -902,6 +988,12 @@ void gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
   if (bn == BN_ && a.epi == EPI_) {                                       \
     launch_impl<BN_, ST_, EPI_, true>(ta, tb, p, grid, stream);           \
     return;                                                               \
+  }
+  if (a.fp8 && a.w8 == 5) {
+    if (bn == 16) { launch_impl<16, 8, EPI_F32_RED_T, true, 5>(ta, tb, p, grid, stream); return; }
+    if (bn == 32) { launch_impl<32, 8, EPI_F32_RED_T, true, 5>(ta, tb, p, grid, stream); return; }
+    if (bn == 64) { launch_impl<64, 8, EPI_F32_RED_T, true, 5>(ta, tb, p, grid, stream); return; }
+    throw std::invalid_argument("gemm (block-scaled fp8): N tile must be 16, 32 or 64");
   }
   if (a.fp8) {
     B200_GEMM_FP8_CASE(256, 4, EPI_BF16)

@@ -121,6 +121,40 @@ __global__ void __launch_bounds__(256) rmsnorm_quant_kernel(const __nv_bfloat16*
   }
 }
 
+// Per-token, per-128-column block quantization (the activations of the block-scaled W8A8 GEMM):
+// one warp per (row, block): s = max|x| / 448 over the block's 128 values (1 for an all-zero
+// block), out = satfinite(x / s), s written to scales[row * lds + block].
+__global__ void __launch_bounds__(256) quant_fp8_block_kernel(const __nv_bfloat16* __restrict__ x,
+                                                              long long ldx, uint8_t* __restrict__ out,
+                                                              long long ldo, float* __restrict__ scales,
+                                                              int lds, int nblk) {
+  pdl_trigger();
+  pdl_wait();
+  const long long r = blockIdx.x;
+  const int b = blockIdx.y * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (b >= nblk) return;
+  const int c = b * 128 + lane * 4;
+  const uint2 v = *reinterpret_cast<const uint2*>(x + r * ldx + c);
+  const float2 a = unpack_bf16x2(v.x), d = unpack_bf16x2(v.y);
+  float m = fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(d.x), fabsf(d.y)));
+  m = warp_max(m);
+  const float sc = m > 0.f ? m / 448.f : 1.f;
+  const float inv = 1.f / sc;
+  *reinterpret_cast<uint32_t*>(out + r * ldo + c) = q4(a.x * inv, a.y * inv, d.x * inv, d.y * inv);
+  if (lane == 0) scales[r * lds + b] = sc;
+}
+
+void quant_fp8_block_launch(const __nv_bfloat16* x, long long ldx, uint8_t* out, long long ldo,
+                            float* scales, int lds, int rows, int cols, cudaStream_t stream) {
+  if (rows == 0) return;
+  if (cols % 128 != 0 || ldx % 4 != 0 || ldo % 4 != 0 || lds < cols / 128)
+    throw std::invalid_argument("quant_fp8_block: columns must be a multiple of 128");
+  const int nblk = cols / 128;
+  launch_pdl(quant_fp8_block_kernel, dim3(rows, (nblk + 7) / 8), dim3(256), 0, stream, x, ldx, out, ldo,
+             scales, lds, nblk);
+}
+
 void quant_fp8_launch(const __nv_bfloat16* x, long long ldx, uint8_t* out, long long ldo, int rows,
                       int cols, float inv_scale, cudaStream_t stream) {
   if (rows == 0) return;

@@ -31,9 +31,18 @@ def _rel(a, b):
     return float((a - b).norm() / (b.norm() + 1e-12))
 
 
+@pytest.fixture
+def w8a16():
+    prev = L.fp8_block_activations()
+    L.set_fp8_block_activations("bf16")
+    yield
+    L.set_fp8_block_activations(prev)
+
+
 @pytest.mark.parametrize("M,N,K", [(1, 1024, 4096), (16, 768, 4096), (64, 4096, 1024),
                                    (128, 3584, 8192), (64, 1280, 3584), (33, 200, 320)])
-def test_block_fp8_decode_accumulate(cuda_device, M, N, K):
+def test_block_fp8_decode_accumulate(cuda_device, w8a16, M, N, K):
+    """W8A16 (exact bf16 activations, weights widened in shared memory)."""
     w = _w(N, K, cuda_device, seed=M + N)
     x = (torch.randn(M, K, device=cuda_device) * 0.5).to(torch.bfloat16)
     acc = torch.zeros(M, N, dtype=torch.float32, device=cuda_device)
@@ -41,6 +50,29 @@ def test_block_fp8_decode_accumulate(cuda_device, M, N, K):
     torch.cuda.synchronize()
     ref = x.float() @ w.dequant_bf16_ref().float().t()
     assert _rel(acc, ref) < 2e-3
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 1024, 4096), (16, 768, 4096), (64, 4096, 1024),
+                                   (7, 28672, 4096), (64, 1280, 8192), (48, 10240, 8192)])
+def test_block_fp8_decode_w8a8(cuda_device, M, N, K):
+    """W8A8 with per-k-block promotion: against the fp32 product of the dequantized weights and
+    the dequantized per-block e4m3 activations (tight), and against the unquantized activations
+    (the activation rounding only).  Repeated launches reuse the zeroed accumulator."""
+    assert L.fp8_block_activations() == "fp8"
+    w = _w(N, K, cuda_device, seed=M + N + 1)
+    x = (torch.randn(M, K, device=cuda_device) * 0.5).to(torch.bfloat16)
+    xq, xs = L.quantize_fp8_blocks(x)
+    xq_ref, xs_ref = L.quantize_fp8_blocks(x.cpu())
+    assert torch.allclose(xs.cpu(), xs_ref, rtol=1e-6)
+    wd = w.dequant_bf16_ref().float()
+    ref_q = L.dequantize_fp8_blocks(xq, xs).float() @ wd.t()
+    ref = x.float() @ wd.t()
+    for _ in range(2):
+        acc = torch.zeros(M, N, dtype=torch.float32, device=cuda_device)
+        L.gemm_accumulate(x, w, acc)
+        torch.cuda.synchronize()
+        assert _rel(acc, ref_q) < 2e-3
+        assert _rel(acc, ref) < 4e-2
 
 
 @pytest.mark.parametrize("M,N,K", [(300, 1024, 4096), (1024, 4096, 1024), (2048, 1536, 2048),

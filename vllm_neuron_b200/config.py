@@ -191,6 +191,9 @@ class B200Config:
     fused_comm: bool = True           # fused GEMM+collective kernels (else NCCL baseline)
     fused_sp: bool = False            # sequence-parallel prefill on the fused RS/AG GEMMs (else NCCL)
     use_cublas_baseline: bool = False  # library GEMMs instead of the tcgen05 kernels
+    # decode-size block-FP8 projections: "fp8" quantizes activations per token and 128-wide k
+    # block (W8A8 on the tensor cores), "bf16" keeps them exact (W8A16)
+    fp8_block_activations: str = "fp8"
     sampling_dp: bool = False          # TP decode: each rank samples 1/W of the rows (all-to-all)
     vision_tp_size: int = 1            # vision encoder sharded over this many consecutive TP ranks
     extra: dict = field(default_factory=dict)
@@ -237,6 +240,8 @@ class B200Config:
                 if not all(isinstance(x, int) and x > 0 for x in v):
                     raise ValueError(f"{name} must be a list of positive integers")
                 setattr(self, name, sorted(set(v)))
+        if self.fp8_block_activations not in ("fp8", "bf16"):
+            raise ValueError(f"fp8_block_activations must be 'fp8' or 'bf16', got {self.fp8_block_activations!r}")
         if self.all2all_backend not in (None, "neuron", "nvlink", "nccl"):
             raise ValueError(f"unknown all2all_backend {self.all2all_backend!r}")
         if self.quantization not in (None, "fp8", "fp8_static", "fp8_block", "mxfp4", "mxfp8",

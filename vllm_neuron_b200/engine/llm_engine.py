@@ -137,6 +137,7 @@ def build_model(args: EngineArgs, tp: GroupComm = SINGLE):
     from ..ops import linear as _lin
 
     _lin.set_library_gemm(b200_config.use_cublas_baseline)
+    _lin.set_fp8_block_activations(b200_config.fp8_block_activations)
     if b200_config.sequence_parallel and hasattr(model, "sequence_parallel"):
         model.sequence_parallel = True
     if (real_group and device.type == "cuda" and b200_config.fused_comm

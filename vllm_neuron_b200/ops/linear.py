@@ -221,6 +221,49 @@ def library_gemm() -> bool:
 def _lib(x: torch.Tensor, w) -> bool:
     return _LIBRARY_GEMM and x.is_cuda and isinstance(w, torch.Tensor)
 
+
+# Activations of decode-size block-FP8 projections: "fp8" quantizes them per token and 128-wide k
+# block (W8A8, per-k-block promotion on the tensor cores: the weight stream needs no widening),
+# "bf16" keeps them exact (W8A16: the weight tiles are widened to bf16 in shared memory).
+_FP8_BLOCK_ACT = "fp8"
+
+
+def set_fp8_block_activations(mode: str) -> None:
+    global _FP8_BLOCK_ACT
+    if mode not in ("fp8", "bf16"):
+        raise ValueError(f"fp8 block activations must be 'fp8' or 'bf16', got {mode!r}")
+    _FP8_BLOCK_ACT = mode
+
+
+def fp8_block_activations() -> str:
+    return _FP8_BLOCK_ACT
+
+
+def quantize_fp8_blocks(x: torch.Tensor, out: torch.Tensor | None = None,
+                        scales: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-token, per-128-column e4m3 quantization: ``s = max|x_block| / 448`` (1 for an
+    all-zero block), ``q = satfinite(x / s)``.  Returns ``(q [M, K], s [M, K / 128])``."""
+    M, K = x.shape
+    assert K % 128 == 0
+    if out is None:
+        out = torch.empty((M, K), dtype=torch.float8_e4m3fn, device=x.device)
+    if scales is None:
+        scales = torch.empty((M, K // 128), dtype=torch.float32, device=x.device)
+    if x.is_cuda and x.dtype == torch.bfloat16 and x.stride(1) == 1:
+        ext().quant_fp8_block(x, out, scales)
+        return out, scales
+    xb = x.float().view(M, K // 128, 128)
+    s = xb.abs().amax(-1)
+    s = torch.where(s > 0, s / FP8_MAX, torch.ones_like(s))
+    out.copy_((xb / s[..., None]).clamp(-FP8_MAX, FP8_MAX).view(M, K).to(torch.float8_e4m3fn))
+    scales.copy_(s)
+    return out, scales
+
+
+def dequantize_fp8_blocks(q: torch.Tensor, s: torch.Tensor) -> torch.Tensor:
+    M, K = q.shape
+    return (q.float().view(M, K // 128, 128) * s[..., None]).view(M, K)
+
 _NUM_SMS: dict[int, int] = {}
 
 
@@ -348,7 +391,14 @@ def gemm_accumulate(x: torch.Tensor, w: torch.Tensor, acc: torch.Tensor,
             acc[:M].add_(x.float() @ w.dequant_bf16_ref().float().t())
             return acc
         sms = num_sms(x.device)
-        if M <= SKINNY_MAX:
+        if (M <= 64 and _FP8_BLOCK_ACT == "fp8" and K % 128 == 0 and N % 128 == 0 and not splits
+                and w.scales.shape[1] >= K // 128):
+            # W8A8: e4m3 weights and per-block e4m3 activations straight into the tensor cores
+            xq, xs = quantize_fp8_blocks(x)
+            tiles = math.ceil(N / 128)
+            s = pick_splits(N, K, sms, 128) if tiles < sms else -1
+            ext().gemm_fp8_block(w.q, xq, acc, skinny_bn(M), s, w.scales, xs)
+        elif M <= SKINNY_MAX:
             s = splits if splits is not None else pick_splits(N, K, sms)
             ext().gemm_w8(w.q, x, acc, EPI_F32_RED_T, skinny_bn(M), s, w.scales, 1, None, None)
         else:
