@@ -96,6 +96,27 @@ def bench_gemms(tp: int):
     return rows
 
 
+def bench_gemms_decode_splits(tp: int):
+    """Decode projections (64 and 16 tokens) under the split choices of the fp32-reduction
+    kernel: the automatic pick, stream-K (-1) and fixed split-K factors, next to cuBLAS."""
+    H, I, Hq, Hkv, D = 4096, 14336, 32, 8, 128
+    shapes = {"qkv": ((Hq + 2 * Hkv) * D // tp, H), "o_proj": (H, Hq * D // tp),
+              "gate_up": (2 * I // tp, H), "down": (H, I // tp)}
+    rows = []
+    for M in (64, 16):
+        for name, (N, K) in shapes.items():
+            x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+            w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.02
+            acc = torch.zeros(M, N, device="cuda", dtype=torch.float32)
+            r = {"op": f"decode_{name}", "M": M, "N": N, "K": K,
+                 "cublas_us": timeit(lambda: torch.matmul(x, w.t())) * 1e3}
+            for sp in (None, -1, 2, 3, 4, 6, 8):
+                r[f"splits_{sp}_us"] = timeit(lambda: L.gemm_accumulate(x, w, acc, splits=sp)) * 1e3
+            print(json.dumps(r), flush=True)
+            rows.append(r)
+    return rows
+
+
 def bench_gemms_fp8(tp: int):
     """Static FP8 (W8A8) projections of the Llama-3-8B shapes next to the bf16 kernels: the time
     includes the activation quantization kernel; bytes count the fp8 weight."""
@@ -121,6 +142,39 @@ def bench_gemms_fp8(tp: int):
             rows.append({"op": f"gemm_fp8_{name}", "M": M, "N": N, "K": K, "fp8_ms": t8, "bf16_ms": t16,
                          "fp8_tflops": 2.0 * M * N * K / t8 / 1e9, "fp8_weight_gbs": N * K / t8 / 1e6,
                          "speedup_vs_bf16": t16 / t8})
+            print(json.dumps(rows[-1]), flush=True)
+    return rows
+
+
+def bench_gemms_fp8_block(tp: int):
+    """128 x 128 block-FP8 weights (Llama-3-70B shapes per TP shard): W8A16 (weights widened to
+    bf16 in shared memory) against W8A8 (1 x 128 fp8 activation blocks, per-k-block promotion),
+    activation quantization included; bytes count the fp8 weight."""
+    H, I, Hq, Hkv, D = 8192, 28672, 64, 8, 128
+    shapes = {"qkv": ((Hq + 2 * Hkv) * D // tp, H), "o_proj": (H, Hq * D // tp),
+              "gate_up": (2 * I // tp, H), "down": (H, I // tp)}
+    rows = []
+    dev = "cuda"
+    prev = L.fp8_block_activations()
+    for M in (4096, 64, 16):
+        for name, (N, K) in shapes.items():
+            x = torch.randn(M, K, device=dev, dtype=torch.bfloat16)
+            bw = L.BlockFP8Weight.from_weight(torch.randn(N, K, device=dev, dtype=torch.bfloat16) * 0.02)
+            if M > L.SKINNY_MAX:
+                out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+                fn = lambda: L.gemm_out(x, bw, out)
+            else:
+                acc = torch.zeros(M, N, device=dev, dtype=torch.float32)
+                fn = lambda: L.gemm_accumulate(x, bw, acc)
+            t = {}
+            for mode in ("bf16", "fp8"):
+                L.set_fp8_block_activations(mode)
+                t[mode] = timeit(fn)
+            L.set_fp8_block_activations(prev)
+            rows.append({"op": f"gemm_fp8_block_{name}", "M": M, "N": N, "K": K,
+                         "w8a16_ms": t["bf16"], "w8a8_ms": t["fp8"],
+                         "w8a8_tflops": 2.0 * M * N * K / t["fp8"] / 1e9,
+                         "w8a8_weight_gbs": N * K / t["fp8"] / 1e6, "speedup": t["bf16"] / t["fp8"]})
             print(json.dumps(rows[-1]), flush=True)
     return rows
 
@@ -325,8 +379,12 @@ def main():
     only = a.only.split(",")
     if "gemm" in only:
         rows += bench_gemms(a.tp)
+    if "gemmdec" in only:
+        rows += bench_gemms_decode_splits(a.tp)
     if "fp8gemm" in only:
         rows += bench_gemms_fp8(a.tp)
+    if "fp8block" in only:
+        rows += bench_gemms_fp8_block(a.tp)
     if "decode" in only:
         rows += bench_decode_attention(a.tp)
     if "prefill" in only:

@@ -255,6 +255,47 @@ void gemm_fp8_block(const at::Tensor& w, const at::Tensor& xq, at::Tensor& out, 
   check_launch("gemm_fp8_block");
 }
 
+// Block-scaled FP8 W8A8 prefill GEMM: out[m, n] = sum_k xq[m, k] w[n, k] * xs[m, k / 128] *
+// ws[n / 128, k / 128] (bf16 store; tokens as the 128-row operand, 128-wide weight tiles).
+void gemm_fp8_block_prefill(const at::Tensor& xq, const at::Tensor& w, at::Tensor& out,
+                            const at::Tensor& w_scales, const at::Tensor& x_scales) {
+  CHECK_CUDA(w);
+  CHECK_CUDA(xq);
+  CHECK_BF16(out);
+  TORCH_CHECK(w.scalar_type() == at::kFloat8_e4m3fn && xq.scalar_type() == at::kFloat8_e4m3fn,
+              "gemm_fp8_block_prefill: operands must be float8_e4m3fn");
+  TORCH_CHECK(w.dim() == 2 && xq.dim() == 2 && w.size(1) == xq.size(1), "gemm_fp8_block_prefill: bad shapes");
+  TORCH_CHECK(w.stride(1) == 1 && xq.stride(1) == 1 && out.stride(1) == 1, "gemm_fp8_block_prefill: inner dims");
+  TORCH_CHECK(w_scales.scalar_type() == at::kFloat && x_scales.scalar_type() == at::kFloat &&
+                  w_scales.stride(1) == 1 && x_scales.stride(1) == 1,
+              "gemm_fp8_block_prefill: scales must be fp32 with contiguous rows");
+  const c10::cuda::CUDAGuard guard(w.device());
+  b200::GemmArgs g{};
+  g.A = xq.data_ptr();
+  g.B = w.data_ptr();
+  g.out = out.data_ptr();
+  g.lda = xq.stride(0);
+  g.ldb = w.stride(0);
+  g.ldo = out.stride(0);
+  g.M = (int)xq.size(0);
+  g.N = (int)w.size(0);
+  g.K = (int)w.size(1);
+  g.bn = 128;
+  g.epi = b200::EPI_BF16;
+  g.splits = 1;
+  g.status = status_word();
+  g.fp8 = 1;
+  g.w8 = 5;
+  g.w_scales = w_scales.data_ptr<float>();
+  g.w_scale_ld = (int)w_scales.stride(0);
+  g.w_scale_rows = (int)w_scales.size(0);
+  g.x_scales = x_scales.data_ptr<float>();
+  g.x_scale_ld = (int)x_scales.stride(0);
+  if (g.M == 0 || g.N == 0) return;
+  b200::gemm_bf16_launch(g, cur_stream());
+  check_launch("gemm_fp8_block_prefill");
+}
+
 // FP8 (e4m3) GEMM with per-tensor scales: out = alpha * (a @ b^T) (epilogue as in `gemm`).
 void gemm_fp8(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, int64_t epi, int64_t bn,
               int64_t splits, double alpha) {
@@ -1147,6 +1188,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_sp", &gemm_sp);
   m.def("gemm_fp8", &gemm_fp8);
   m.def("gemm_fp8_block", &gemm_fp8_block);
+  m.def("gemm_fp8_block_prefill", &gemm_fp8_block_prefill);
   m.def("quant_fp8_block", &quant_fp8_block);
   m.def("quant_fp8", &quant_fp8);
   m.def("rmsnorm_quant", &rmsnorm_quant);

@@ -251,8 +251,9 @@ __global__ void __launch_bounds__((W8 >= 1 && W8 <= 4) ? 320 : 192, 1)
   constexpr int kBTileBytes = BN * kBK * 2;
   constexpr bool kConv = W8 >= 1 && W8 <= 4;                 // converter warps widen the weight
   constexpr bool kPromote = W8 == 5;                         // block-scaled FP8, per-k-block sums
-  static_assert(!kPromote || (FP8 && EPI == EPI_F32_RED_T && BN <= 64),
-                "promotion mode: FP8 operands, swapped decode layout, N tile <= 64");
+  static_assert(!kPromote || (FP8 && ((EPI == EPI_F32_RED_T && BN <= 64) || (EPI == EPI_BF16 && BN == 128))),
+                "promotion mode: FP8 operands; swapped decode layout with N tile <= 64, or tokens as A "
+                "with a 128-wide weight tile");
   constexpr bool kFP4 = W8 == 3 || W8 == 4;                  // MXFP4 (else block FP8)
   constexpr int kWSide = !kConv ? 0 : (W8 == 1 || W8 == 3) ? 1 : 2;  // weight operand: A / B
   constexpr int kW8Rows = kWSide == 1 ? kBM : kWSide == 2 ? BN : 0;  // weight rows per tile
@@ -597,9 +598,11 @@ __global__ void __launch_bounds__((W8 >= 1 && W8 <= 4) ? 320 : 192, 1)
       bool ok = true;
       while (ok && cur.next(p, mb, nb, k0, k1)) {
         const TileRows trows = tile_rows(p, mb);
-        const int m = trows.a_row + row;  // weight row = output column
-        const int n_base = nb * BN;       // first token of the tile
-        const float* wsc_row = p.wsc + (long long)min(trows.a_row >> 7, p.wsc_rows - 1) * p.wsc_ld;
+        const int m = trows.a_row + row;  // swapped: weight row = output column; else token row
+        const int n_base = nb * BN;       // swapped: first token; else first weight row (column)
+        constexpr bool kSwapped = EPI == EPI_F32_RED_T;
+        const float* wsc_row =
+            p.wsc + (long long)min((kSwapped ? trows.a_row : n_base) >> 7, p.wsc_rows - 1) * p.wsc_ld;
         float racc[BN];
 #pragma unroll
         for (int j = 0; j < BN; ++j) racc[j] = 0.f;
@@ -612,16 +615,29 @@ __global__ void __launch_bounds__((W8 >= 1 && W8 <= 4) ? 320 : 192, 1)
           tc_fence_after();
           const float sw = __ldg(wsc_row + kb);
           const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + pa * BN;
+          if constexpr (kSwapped) {
 #pragma unroll
-          for (int c = 0; c < BN; c += 16) {
-            uint32_t r[16];
-            tmem_ld_32x32b_x16(t_row + c, r);
-            tmem_ld_wait();
+            for (int c = 0; c < BN; c += 16) {
+              uint32_t r[16];
+              tmem_ld_32x32b_x16(t_row + c, r);
+              tmem_ld_wait();
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const int n = n_base + c + j;
-              const float sx = n < p.N ? __ldg(p.xsc + (long long)n * p.xsc_ld + kb) : 0.f;
-              racc[c + j] = fmaf(__uint_as_float(r[j]), sw * sx, racc[c + j]);
+              for (int j = 0; j < 16; ++j) {
+                const int n = n_base + c + j;  // the token's scale per column
+                const float sx = n < p.N ? __ldg(p.xsc + (long long)n * p.xsc_ld + kb) : 0.f;
+                racc[c + j] = fmaf(__uint_as_float(r[j]), sw * sx, racc[c + j]);
+              }
+            }
+          } else {
+            // one factor per row: this token's activation scale times the weight block's
+            const float f = sw * (m < p.M ? __ldg(p.xsc + (long long)m * p.xsc_ld + kb) : 0.f);
+#pragma unroll
+            for (int c = 0; c < BN; c += 32) {
+              uint32_t r[32];
+              tmem_ld_32x32b_x32(t_row + c, r);
+              tmem_ld_wait();
+#pragma unroll
+              for (int j = 0; j < 32; ++j) racc[c + j] = fmaf(__uint_as_float(r[j]), f, racc[c + j]);
             }
           }
           tc_fence_before();
@@ -629,11 +645,26 @@ __global__ void __launch_bounds__((W8 >= 1 && W8 <= 4) ? 320 : 192, 1)
           if (lane == 0) mbar_arrive(&tempty_bar[pa]);
         }
         if (!ok) break;
-        if (m < trows.m_lim) {
-          float* o = reinterpret_cast<float*>(p.out) + m;
+        if constexpr (kSwapped) {
+          if (m < trows.m_lim) {
+            float* o = reinterpret_cast<float*>(p.out) + m;
 #pragma unroll
-          for (int j = 0; j < BN; ++j)
-            if (n_base + j < p.N) atomicAdd(o + (long long)(n_base + j) * p.ldo, racc[j]);
+            for (int j = 0; j < BN; ++j)
+              if (n_base + j < p.N) atomicAdd(o + (long long)(n_base + j) * p.ldo, racc[j]);
+          }
+        } else if (m < trows.m_lim) {
+          __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + (long long)m * p.ldo + n_base;
+          if (n_base + BN <= p.N && (p.ldo % 8) == 0) {
+#pragma unroll
+            for (int c = 0; c < BN; c += 8)
+              *reinterpret_cast<uint4*>(o + c) =
+                  make_uint4(pack_bf16x2(racc[c], racc[c + 1]), pack_bf16x2(racc[c + 2], racc[c + 3]),
+                             pack_bf16x2(racc[c + 4], racc[c + 5]), pack_bf16x2(racc[c + 6], racc[c + 7]));
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN; ++j)
+              if (n_base + j < p.N) o[j] = __float2bfloat16(racc[j]);
+          }
         }
       }
     } else
@@ -914,11 +945,17 @@ void gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
     if ((uint64_t)a.w_scale_rows < wrows)
       throw std::invalid_argument("gemm: MXFP4 scale rows do not cover the weight rows");
   } else if (a.w8 == 5) {
-    if (!a.fp8 || a.w_scales == nullptr || a.x_scales == nullptr || a.epi != EPI_F32_RED_T || grouped ||
-        a.sp != nullptr || a.K % 128 != 0 || a.M % 128 != 0 || a.w_scale_ld < a.K / 128 ||
-        a.x_scale_ld < a.K / 128 || (uint64_t)a.w_scale_rows < (uint64_t)a.M / 128)
-      throw std::invalid_argument("gemm: block-scaled FP8 W8A8 needs e4m3 operands, weight (A) and "
-                                  "activation (B) block scales, EPI_F32_RED_T, K and weight rows in 128s");
+    // swapped decode layout (EPI_F32_RED_T): weights = A, tokens = B; prefill (EPI_BF16): tokens
+    // = A, weights = B with a 128-wide N tile
+    const bool swapped = a.epi == EPI_F32_RED_T;
+    const int wrows = swapped ? a.M : a.N;
+    if (!a.fp8 || a.w_scales == nullptr || a.x_scales == nullptr || (!swapped && a.epi != EPI_BF16) ||
+        (!swapped && a.bn != 128) || grouped || a.sp != nullptr || a.K % 128 != 0 || wrows % 128 != 0 ||
+        a.w_scale_ld < a.K / 128 || a.x_scale_ld < a.K / 128 || a.w_scale_rows < wrows / 128 ||
+        (!swapped && a.splits > 1))
+      throw std::invalid_argument("gemm: block-scaled FP8 W8A8 needs e4m3 operands, weight and activation "
+                                  "block scales, EPI_F32_RED_T (weights as A) or EPI_BF16 with bn 128 "
+                                  "(weights as B), K and weight rows in 128s");
   } else if (a.w8 != 0) {
     throw std::invalid_argument("gemm: w8 must be 0..5");
   }
@@ -990,6 +1027,7 @@ void gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
     return;                                                               \
   }
   if (a.fp8 && a.w8 == 5) {
+    if (a.epi == EPI_BF16) { launch_impl<128, 6, EPI_BF16, true, 5>(ta, tb, p, grid, stream); return; }
     if (bn == 16) { launch_impl<16, 8, EPI_F32_RED_T, true, 5>(ta, tb, p, grid, stream); return; }
     if (bn == 32) { launch_impl<32, 8, EPI_F32_RED_T, true, 5>(ta, tb, p, grid, stream); return; }
     if (bn == 64) { launch_impl<64, 8, EPI_F32_RED_T, true, 5>(ta, tb, p, grid, stream); return; }

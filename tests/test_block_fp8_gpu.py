@@ -52,8 +52,8 @@ def test_block_fp8_decode_accumulate(cuda_device, w8a16, M, N, K):
     assert _rel(acc, ref) < 2e-3
 
 
-@pytest.mark.parametrize("M,N,K", [(1, 1024, 4096), (16, 768, 4096), (64, 4096, 1024),
-                                   (7, 28672, 4096), (64, 1280, 8192), (48, 10240, 8192)])
+@pytest.mark.parametrize("M,N,K", [(1, 1024, 4096), (16, 768, 4096), (32, 4096, 1024),
+                                   (7, 28672, 4096), (32, 1280, 8192), (24, 10240, 8192)])
 def test_block_fp8_decode_w8a8(cuda_device, M, N, K):
     """W8A8 with per-k-block promotion: against the fp32 product of the dequantized weights and
     the dequantized per-block e4m3 activations (tight), and against the unquantized activations
@@ -77,7 +77,8 @@ def test_block_fp8_decode_w8a8(cuda_device, M, N, K):
 
 @pytest.mark.parametrize("M,N,K", [(300, 1024, 4096), (1024, 4096, 1024), (2048, 1536, 2048),
                                    (129, 384, 640)])
-def test_block_fp8_prefill_out(cuda_device, M, N, K):
+def test_block_fp8_prefill_out(cuda_device, w8a16, M, N, K):
+    """W8A16 prefill (weights widened in shared memory, exact bf16 activations)."""
     w = _w(N, K, cuda_device, seed=M)
     x = (torch.randn(M, K, device=cuda_device) * 0.5).to(torch.bfloat16)
     for bn in (128, 256):
@@ -87,7 +88,7 @@ def test_block_fp8_prefill_out(cuda_device, M, N, K):
         assert _rel(out, ref) < 1e-2, bn
 
 
-def test_block_fp8_prefill_silu_and_splitk(cuda_device):
+def test_block_fp8_prefill_silu_and_splitk(cuda_device, w8a16):
     I, K, M = 1024, 2048, 512
     g = _w(I, K, cuda_device, seed=7).dequant_bf16_ref()
     u = _w(I, K, cuda_device, seed=8).dequant_bf16_ref()
@@ -122,6 +123,27 @@ def test_block_fp8_grouped_experts(cuda_device):
     for e, a, b in ((2, 0, 100), (0, 128, 300), (3, 384, 512)):
         ref = x[a:b].float() @ wd[e].t()
         assert _rel(out[a:b], ref) < 1e-2, (e, a, b)
+
+
+@pytest.mark.parametrize("M,N,K", [(300, 1024, 4096), (1024, 4096, 1024), (2048, 1536, 2048),
+                                   (129, 384, 640), (4096, 28672, 8192)])
+def test_block_fp8_prefill_w8a8(cuda_device, M, N, K):
+    """W8A8 prefill with per-k-block promotion (tokens as the 128-row operand, 128-wide weight
+    tiles, bf16 store): against the dequantized-activation oracle (tight) and the exact one."""
+    assert L.fp8_block_activations() == "fp8"
+    w = _w(N, K, cuda_device, seed=M + 3)
+    x = (torch.randn(M, K, device=cuda_device) * 0.5).to(torch.bfloat16)
+    xq, xs = L.quantize_fp8_blocks(x)
+    wd = w.dequant_bf16_ref().float()
+    ref_q = L.dequantize_fp8_blocks(xq, xs).float() @ wd.t()
+    out = L.gemm_out(x, w)
+    torch.cuda.synchronize()
+    assert _rel(out, ref_q) < 5e-3
+    assert _rel(out, x.float() @ wd.t()) < 4e-2
+    if N % 256 == 0:  # the SwiGLU form: gate/up through the same kernel, then the activation
+        y = L.gemm_silu(x, w)
+        torch.cuda.synchronize()
+        assert _rel(y, L.silu_mul_ref(ref_q, L.SILU_BLOCK)) < 1e-2
 
 
 def test_block_fp8_linear_layer_of_model(cuda_device):
