@@ -171,6 +171,14 @@ def bench_gemms_fp8_block(tp: int):
                 L.set_fp8_block_activations(mode)
                 t[mode] = timeit(fn)
             L.set_fp8_block_activations(prev)
+            if M <= L.SKINNY_MAX:
+                # the W8A8 kernel itself at every decode size (the op routes W8A8 up to 32 tokens)
+                def w8a8_direct():
+                    xq, xs = L.quantize_fp8_blocks(x)
+                    tiles = -(-N // 128)
+                    sp = L.pick_splits(N, K, L.num_sms(x.device), 128) if tiles < L.num_sms(x.device) else -1
+                    ext().gemm_fp8_block(bw.q, xq, acc, L.skinny_bn(M), sp, bw.scales, xs)
+                t["fp8"] = timeit(w8a8_direct)
             rows.append({"op": f"gemm_fp8_block_{name}", "M": M, "N": N, "K": K,
                          "w8a16_ms": t["bf16"], "w8a8_ms": t["fp8"],
                          "w8a8_tflops": 2.0 * M * N * K / t["fp8"] / 1e9,

@@ -264,7 +264,10 @@ __global__ void __launch_bounds__((W8 >= 1 && W8 <= 4) ? 320 : 192, 1)
   constexpr int kStageTx = kWSide == 1   ? kSBytes + kBTileBytes
                            : kWSide == 2 ? kATileBytes + kSBytes
                                          : kATileBytes + kBTileBytes;
-  constexpr uint32_t kTmemCols = TmemCols<BN>::v;
+  // accumulator buffers: 2 tiles in flight; the promotion mode keeps 4 k-block accumulators so
+  // the MMA issuer runs up to 4 k blocks ahead of the promoting epilogue
+  constexpr int kAccBufs = kPromote ? 4 : 2;
+  constexpr uint32_t kTmemCols = kPromote ? TmemCols<2 * BN>::v : TmemCols<BN>::v;
   constexpr uint32_t kIdesc = make_idesc_f16(kBM, BN, !FP8);  // FP8: type fields 0 = E4M3
   constexpr int kKElems = FP8 ? 2 * kBK : kBK;                  // elements per k-block
 
@@ -279,8 +282,8 @@ __global__ void __launch_bounds__((W8 >= 1 && W8 <= 4) ? 320 : 192, 1)
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* conv_bar = empty_bar + STAGES;  // converted operand ready (W8)
   uint64_t* tfull_bar = conv_bar + STAGES;
-  uint64_t* tempty_bar = tfull_bar + 2;
-  uint32_t* tmem_base_smem = reinterpret_cast<uint32_t*>(tempty_bar + 2);
+  uint64_t* tempty_bar = tfull_bar + kAccBufs;
+  uint32_t* tmem_base_smem = reinterpret_cast<uint32_t*>(tempty_bar + kAccBufs);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_smem + 1);
   unsigned int* rs_arrivals = tmem_base_smem + 2;  // epilogue threads done with their RS stores
 
@@ -298,7 +301,7 @@ __global__ void __launch_bounds__((W8 >= 1 && W8 <= 4) ? 320 : 192, 1)
       mbar_init(&empty_bar[s], 1);
       mbar_init(&conv_bar[s], 4);
     }
-    for (int a = 0; a < 2; ++a) {
+    for (int a = 0; a < kAccBufs; ++a) {
       mbar_init(&tfull_bar[a], 1);
       mbar_init(&tempty_bar[a], 4);
     }
@@ -433,8 +436,8 @@ __global__ void __launch_bounds__((W8 >= 1 && W8 <= 4) ? 320 : 192, 1)
           const uint32_t ph = (it / STAGES) & 1;
           if constexpr (kPromote) {
             // each k block into its own accumulator, once the epilogue has drained it
-            const int pa = u & 1;
-            if (!mbar_wait_abortable(&tempty_bar[pa], ((u >> 1) & 1) ^ 1, kTimeoutTmemEmpty, p.status,
+            const int pa = u % kAccBufs;
+            if (!mbar_wait_abortable(&tempty_bar[pa], ((u / kAccBufs) & 1) ^ 1, kTimeoutTmemEmpty, p.status,
                                      abort_flag, wait_ns)) {
               ok = false;
               break;
@@ -461,7 +464,7 @@ __global__ void __launch_bounds__((W8 >= 1 && W8 <= 4) ? 320 : 192, 1)
           }
           umma_commit(&empty_bar[s]);
           if constexpr (kPromote) {
-            umma_commit(&tfull_bar[u & 1]);
+            umma_commit(&tfull_bar[u % kAccBufs]);
             ++u;
           }
         }
@@ -607,8 +610,8 @@ __global__ void __launch_bounds__((W8 >= 1 && W8 <= 4) ? 320 : 192, 1)
 #pragma unroll
         for (int j = 0; j < BN; ++j) racc[j] = 0.f;
         for (int kb = k0; kb < k1; ++kb, ++u) {
-          const int pa = u & 1;
-          if (!mbar_wait_abortable(&tfull_bar[pa], (u >> 1) & 1, kTimeoutTmemFull, p.status, abort_flag, wait_ns)) {
+          const int pa = u % kAccBufs;
+          if (!mbar_wait_abortable(&tfull_bar[pa], (u / kAccBufs) & 1, kTimeoutTmemFull, p.status, abort_flag, wait_ns)) {
             ok = false;
             break;
           }
@@ -888,7 +891,7 @@ static void launch_impl(const CUtensorMap& ta, const CUtensorMap& tb, const Gemm
                         int grid, cudaStream_t stream) {
   constexpr int w8_rows = (W8 == 1 || W8 == 3) ? kBM : (W8 == 2 || W8 == 4) ? BN : 0;
   constexpr int srow = (W8 == 3 || W8 == 4) ? kBK / 2 : kBK;
-  constexpr int smem = STAGES * (kATileBytes + BN * kBK * 2 + w8_rows * srow) + 1024 + 256;
+  constexpr int smem = STAGES * (kATileBytes + BN * kBK * 2 + w8_rows * srow) + 1024 + 512;
   static_assert(smem <= 232448, "shared memory budget");
   auto kern = gemm_bf16_kernel<BN, STAGES, EPI, FP8, W8>;
   static std::atomic<uint64_t> configured{0};  // per instantiation, per device
