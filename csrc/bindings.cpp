@@ -63,6 +63,14 @@ int64_t read_status() {
   return v;
 }
 void reset_status() { TORCH_CHECK(cudaMemset(status_word(), 0, sizeof(uint32_t)) == cudaSuccess); }
+// Asynchronous read of the status word into a pinned host int32 (ordered on the current
+// stream): lets a serving loop watch for expired device waits without a device sync.
+void status_copy_async(at::Tensor dst) {
+  TORCH_CHECK(!dst.is_cuda() && dst.is_pinned() && dst.scalar_type() == at::kInt && dst.numel() >= 1,
+              "dst must be a pinned host int32 tensor");
+  TORCH_CHECK(cudaMemcpyAsync(dst.data_ptr(), status_word(), sizeof(uint32_t), cudaMemcpyDeviceToHost,
+                              cur_stream()) == cudaSuccess);
+}
 
 // Number of kernels this library has launched (or recorded into a CUDA graph) in this
 // process; the benchmark reports it for its timed region.
@@ -1205,6 +1213,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("read_status", &read_status);
   m.def("flag_wait_probe", &flag_wait_probe);
   m.def("reset_status", &reset_status);
+  m.def("status_copy_async", &status_copy_async);
   m.def("num_sms", &num_sms);
   m.def("launch_count", &launch_count);
   m.def("symm_alloc", &symm_alloc);

@@ -6,6 +6,7 @@ import os
 import socket
 
 import numpy as np
+import pytest
 
 from tests.test_qwen3_vl_cpu import IMG, PROC, VE, VS, _ckpt
 
@@ -96,7 +97,8 @@ def _vision_dp_worker(rank, port, ckpt, q, extra=None):
     try:
         llm = LLM(ckpt, tensor_parallel_size=2, **dict(KW, **(extra or {})))
         outs = llm.generate(_three_image_prompts(), SamplingParams(temperature=0, max_tokens=5, ignore_eos=True))
-        q.put((rank, ([o.outputs[0].token_ids for o in outs], llm.engine.model.vision_calls)))
+        q.put((rank, ([o.outputs[0].token_ids for o in outs], llm.engine.model.vision_calls,
+                     llm.engine.model.vision_blocks)))
     except Exception:  # pragma: no cover
         import traceback
 
@@ -163,3 +165,34 @@ def test_vision_tensor_parallel_over_tp_ranks():
         assert not isinstance(res[r], str), res[r]
     assert res[0][0] == ref and res[1][0] == ref, (res, ref)
     assert res[0][1] == 3 and res[1][1] == 3
+
+
+@pytest.mark.parametrize("vision", [{"vision_attention_block_size": 32},
+                                    {"vision_attention_block_size": 32, "tp_size": 2}])
+def test_packed_vision_over_tp_ranks(vision):
+    """Packed encoder on TP=2: the three images (32, 24 and 16 patches) take three 32-row
+    blocks, padded to four for two replicas; with vision DP (default) each rank encodes two blocks and the merged
+    rows are all-gathered; with vision TP 2 both ranks encode the three blocks on half the heads.
+    Tokens equal the unpacked TP=1 run."""
+    from vllm_neuron_b200.engine.sampling_params import SamplingParams
+    from vllm_neuron_b200.entrypoints import LLM
+
+    d, _ = _ckpt()
+    ref = LLM(d, **KW).generate(_three_image_prompts(),
+                                SamplingParams(temperature=0, max_tokens=5, ignore_eos=True))
+    ref = [o.outputs[0].token_ids for o in ref]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    extra = {"additional_config": {"vision_neuron_config": vision}}
+    procs = [ctx.Process(target=_vision_dp_worker, args=(r, port, d, q, extra)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    for r in (0, 1):
+        assert not isinstance(res[r], str), res[r]
+    assert res[0][0] == ref and res[1][0] == ref, (res, ref)
+    blocks = 3 if vision.get("tp_size", 1) == 2 else 2  # no DP replicas: no padding
+    assert res[0][2] == blocks and res[1][2] == blocks

@@ -101,17 +101,22 @@ def test_mrope_positions_layout():
     assert delta == 6 - 9
 
 
-def test_qwen3_vl_video_matches_hf():
+@pytest.mark.parametrize("packed", [False, True])
+def test_qwen3_vl_video_matches_hf(packed):
     """A 4-frame video (two temporal patch groups, each a timestamp + vision span) next to an
-    image: greedy tokens match HF's forward with pixel_values_videos / video_grid_thw."""
+    image: greedy tokens match HF's forward with pixel_values_videos / video_grid_thw.  With
+    ``packed`` the encoder runs the image and the video's frame groups packed into 64-row
+    blocks (block-local attention bounds)."""
     from vllm_neuron_b200.engine.multimodal import _processor, _video_processor
 
     d, hf = _ckpt()
     rng = np.random.default_rng(3)
     frames = (rng.random((4, 16, 24, 3)) * 255).astype(np.uint8)
     img = (rng.random((16, 16, 3)) * 255).astype(np.uint8)
+    ac = {"vision_neuron_config": {"vision_attention_block_size": 64}} if packed else None
     llm = LLM(d, device="cpu", dtype="float32", max_num_seqs=2, max_model_len=256, num_gpu_blocks=64,
-              max_num_batched_tokens=16, mm_processor_kwargs=PROC, skip_tokenizer_init=True)
+              max_num_batched_tokens=16, mm_processor_kwargs=PROC, skip_tokenizer_init=True,
+              additional_config=ac)
     vc = llm.engine.model.cfg.raw["vision_config"]
     vo = _video_processor(d, vc, PROC)(videos=[frames], return_tensors="pt", do_sample_frames=False,
                                        video_metadata=[{"fps": 2.0, "total_num_frames": 4}])
@@ -139,6 +144,7 @@ def test_qwen3_vl_video_matches_hf():
             ref.append(nxt)
             cur.append(nxt)
     assert got == ref, (got, ref)
+    assert (llm.engine.model.vision_blocks > 0) == packed
 
 
 def test_encoder_cache_reuses_identical_images():

@@ -273,3 +273,102 @@ class B200Config:
             raise ValueError("max_logprobs must be >= 0")
         if self.modules_to_not_convert is not None and not all(isinstance(m, str) for m in self.modules_to_not_convert):
             raise ValueError("modules_to_not_convert must be a list of module names")
+
+
+@dataclass
+class VisionConfig:
+    """Options of the vision encoder, ``additional_config["vision_neuron_config"]``.
+
+    ``vision_attention_block_size`` rows per packed block (images packed first-fit decreasing,
+    attention restricted to each image's frames); ``num_vision_tokens_buckets`` the packed
+    sizes a request's vision tokens are rounded up to (one CUDA graph of the encoder per
+    bucket); default: powers of two from one block up to ``max_vision_seq_len``.
+    ``tp_size`` / ``dp_size``: vision tensor parallelism over consecutive ranks and the number
+    of replicas that split a request's blocks (``tp_size * dp_size`` = the TP world; the one
+    left at 1 is derived).  ``encoder_cache_num_blocks``: vision encodings kept for reuse.
+
+    Reference: vllm_neuron/model/neuron_config.py (``VisionNeuronConfig``: the same keys,
+    ``resolve_tp_dp``), vllm_neuron/vllm/worker/neuron_model_runner.py:456-466.
+    """
+
+    num_vision_tokens_buckets: list | None = None
+    vision_attention_block_size: int = 2048
+    tp_size: int = 1
+    dp_size: int = 1
+    max_vision_seq_len: int | None = None
+    encoder_cache_num_blocks: int | None = None
+    encoder_cache_min_hold_time_ms: float | None = None
+    cuda_graphs: bool = True   # capture the packed encoder per bucket
+
+    KEY = "vision_neuron_config"
+
+    @classmethod
+    def from_dict(cls, d: dict) -> "VisionConfig":
+        known = {f.name for f in dataclasses.fields(cls)}
+        bad = sorted(k for k in d if k not in known)
+        if bad:
+            raise ValueError(f"unknown vision_neuron_config keys {bad} (known: {sorted(known)})")
+        c = cls(**d)
+        c.validate()
+        return c
+
+    @classmethod
+    def from_additional_config(cls, additional: dict | None) -> "VisionConfig | None":
+        d = (additional or {}).get(cls.KEY)
+        return None if d is None else cls.from_dict(dict(d))
+
+    def validate(self):
+        bs = self.vision_attention_block_size
+        if not isinstance(bs, int) or bs < 4 or bs % 4:
+            raise ValueError(f"vision_attention_block_size must be a positive multiple of 4, got {bs!r}")
+        for name in ("tp_size", "dp_size"):
+            v = getattr(self, name)
+            if not isinstance(v, int) or v < 1:
+                raise ValueError(f"vision {name} must be a positive integer, got {v!r}")
+        if self.max_vision_seq_len is None:
+            self.max_vision_seq_len = bs
+        if not isinstance(self.max_vision_seq_len, int) or self.max_vision_seq_len < 1:
+            raise ValueError("max_vision_seq_len must be a positive integer")
+        if self.num_vision_tokens_buckets is not None:
+            b = self.num_vision_tokens_buckets
+            if not b or not all(isinstance(x, int) and x > 0 for x in b):
+                raise ValueError("num_vision_tokens_buckets must be a non-empty list of positive integers")
+            self.num_vision_tokens_buckets = sorted(set(b))
+        else:
+            top = max(bs, -(-self.max_vision_seq_len // bs) * bs)
+            b, n = [], bs
+            while n < top:
+                b.append(n)
+                n *= 2
+            self.num_vision_tokens_buckets = b + [top]
+        if self.encoder_cache_num_blocks is not None and (
+                not isinstance(self.encoder_cache_num_blocks, int) or self.encoder_cache_num_blocks < 1):
+            raise ValueError("encoder_cache_num_blocks must be a positive integer")
+
+    def resolve_tp_dp(self, world: int) -> tuple[int, int]:
+        """Concrete (vision TP, vision DP) for a TP world of ``world`` ranks."""
+        tp, dp = self.tp_size, self.dp_size
+        if tp == 1 and dp == 1:
+            tp, dp = 1, world
+        elif dp == 1:
+            dp = world // tp
+        elif tp == 1:
+            tp = world // dp
+        if tp * dp != world or tp < 1 or dp < 1:
+            raise ValueError(f"vision tp_size {self.tp_size} x dp_size {self.dp_size} does not "
+                             f"match the world of {world} ranks")
+        self.tp_size, self.dp_size = tp, dp
+        return tp, dp
+
+
+def vision_tp_of(additional: dict | None) -> int:
+    """Vision TP degree from either the vision config (``tp_size``) or ``vision_tp_size`` of the
+    framework options (they must agree when both are given)."""
+    a = additional or {}
+    opts = a.get("neuron_config") or a.get("b200_config") or {}
+    legacy = int(opts.get("vision_tp_size", 1))
+    vd = a.get(VisionConfig.KEY) or {}
+    vt = int(vd.get("tp_size", 1))
+    if legacy > 1 and vt > 1 and legacy != vt:
+        raise ValueError(f"vision_tp_size={legacy} and vision_neuron_config.tp_size={vt} disagree")
+    return max(legacy, vt)

@@ -14,7 +14,7 @@ import numpy as np
 import torch
 
 from .. import envs
-from ..config import B200Config, ModelArchConfig
+from ..config import B200Config, ModelArchConfig, VisionConfig, vision_tp_of
 from ..exceptions import DeviceStatusError
 from ..metrics import Metrics
 from ..parallel.comm import SINGLE, GroupComm
@@ -96,14 +96,24 @@ def build_model(args: EngineArgs, tp: GroupComm = SINGLE):
     max_tok = max(args.max_num_batched_tokens, args.max_num_seqs)
     model = cls(arch, tp=tp, device=device, dtype=dtype, max_tokens=max_tok,
                 max_seqs=args.max_num_seqs, block_size=args.block_size)
-    if b200_config.vision_tp_size > 1 and hasattr(model, "set_vision_tp"):
+    vision_tp = vision_tp_of(args.additional_config)
+    if vision_tp > 1 and hasattr(model, "set_vision_tp"):
         from ..parallel import state as _ps
 
         vt = _ps.get_parallel_state().vision_tp
-        if vt.world != b200_config.vision_tp_size:
+        if vt.world != vision_tp:
             raise ValueError("the parallel state has no vision TP group of this size "
                              "(pass the option to the LLM front end)")
         model.set_vision_tp(vt)
+    vcfg = VisionConfig.from_additional_config(args.additional_config)
+    if vcfg is not None:
+        if not hasattr(model, "configure_vision"):
+            raise ValueError(f"vision_neuron_config given for {type(model).__name__}, which has no vision encoder")
+        vcfg.resolve_tp_dp(tp.world)
+        if vcfg.tp_size != model.visual.tp.world:
+            raise ValueError(f"vision tp_size {vcfg.tp_size} does not match the vision TP group "
+                             f"({model.visual.tp.world} ranks)")
+        model.configure_vision(vcfg, cuda_graphs=b200_config.cuda_graphs)
     if args.load_format == "dummy" or model_path is None:
         model.init_random(seed=args.seed)
     else:
@@ -247,6 +257,9 @@ class LLMEngine:
         real_group = tp.world > 1 and tp.group is not None
         self.runner = build_runner(args, self.model, self.max_model_len, self.device, self.b200_config)
         self.runner.sampling_dp = bool(self.b200_config.sampling_dp)
+        vcfg = getattr(self.model, "vision_pack", None)
+        if vcfg is not None and vcfg.encoder_cache_num_blocks:
+            self.runner.encoder_cache_size = vcfg.encoder_cache_num_blocks
         # accuracy tooling: activation capture / golden replacement (eager steps only)
         from ..accuracy.tensor_capture import session_from_config
 
@@ -368,6 +381,20 @@ class LLMEngine:
             self._free_slots.append(req.slot)
             req.slot = -1
 
+    def _watch_device_status(self):
+        """Every step: raise if the status word copied (asynchronously, into pinned memory) after
+        an earlier step shows an expired bounded device wait, then queue the next copy.  A kernel
+        whose wait expired returns without its result, so serving stops at once instead of
+        continuing on garbage (or at one expired wait per launch)."""
+        from ..ops._ext import ext
+
+        host = getattr(self, "_status_host", None)
+        if host is None:
+            host = self._status_host = torch.zeros(1, dtype=torch.int32).pin_memory()
+        elif int(host[0]) != 0:
+            self._check_device_status()
+        ext().status_copy_async(host)
+
     def _check_device_status(self):
         """Raise if a bounded device wait (peer flag of a fused collective) has expired."""
         from ..ops._ext import ext
@@ -461,8 +488,8 @@ class LLMEngine:
         if envs.VLLM_B200_DEBUG_MODE and self.device.type == "cuda":
             torch.cuda.synchronize(self.device)
             self._check_device_status()
-        elif getattr(self.model, "tp_fused", None) is not None and self.num_steps % 16 == 0:
-            self._check_device_status()
+        elif self.device.type == "cuda":
+            self._watch_device_status()
         now = time.perf_counter()
         finished = self.scheduler.update(out, toks, lps, now=now)
         cs = getattr(self.model, "capture", None)

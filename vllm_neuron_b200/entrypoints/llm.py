@@ -13,6 +13,7 @@ from typing import Any, Iterable
 
 import torch
 
+from ..config import vision_tp_of
 from ..engine.llm_engine import EngineArgs, LLMEngine, RequestOutput
 from ..engine.sampling_params import SamplingParams
 from ..parallel import state as ps
@@ -74,7 +75,7 @@ class LLM:
                                                             tensor_parallel_size=tensor_parallel_size,
                                                             data_parallel_size=dp,
                                                             decode_context_parallel_size=decode_context_parallel_size,
-                                                            vision_tp_size=int(_b200_opts(additional_config).get("vision_tp_size", 1))))
+                                                            vision_tp_size=vision_tp_of(additional_config)))
         # Data parallelism: each group of TP ranks is an independent engine replica serving
         # every dp-th request; outputs are gathered over the DP group (reference: data
         # parallel replicas, docs/design/parallelism/data_parallelism.md).

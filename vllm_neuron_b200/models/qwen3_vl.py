@@ -34,6 +34,7 @@ import torch.nn.functional as F
 
 from ..ops import linear as L
 from ..parallel.comm import SINGLE, GroupComm
+from . import vision_packing as VP
 from .llama import LlamaForCausalLM
 
 
@@ -197,34 +198,23 @@ class Qwen3VLVision(torch.nn.Module):
         x = F.gelu(_lin(x, m.fc1_w, m.fc1_b).float()).to(x.dtype)
         return _lin(x, m.fc2_w, m.fc2_b)
 
-    @torch.no_grad()
-    def forward(self, pixels: torch.Tensor, grids: list[tuple[int, int, int]]):
-        """``pixels [N, C * Tp * P * P]`` -> (embeds ``[N / merge^2, out_hidden]``, DeepStack
-        features ``[len(deepstack), N / merge^2, out_hidden]``)."""
+    def _body(self, x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, attend):
+        """The encoder blocks and mergers over rows ``x [R, H]`` (rotary ``cos`` / ``sin``
+        ``[R, head_dim]``); ``attend(q, k, v)`` maps ``[R, heads, hd]`` bf16 tensors to the
+        attention output ``[R, heads * hd]``.  Returns (merged ``[R / merge^2, out_hidden]``,
+        DeepStack ``[n_deep, R / merge^2, out_hidden]``)."""
         dt = self.patch_w.dtype
-        x = _lin(pixels.to(self.patch_w.device, dt), self.patch_w, self.patch_b)
-        x = x + self._pos_embed(grids)
-        cos, sin = self._rotary(grids)
-        lens = [t * h * w for t, h, w in grids]
         H, nh = self.hidden, self.heads_l
         hd = H // self.heads
-        Hl = nh * hd
         deep = []
+        c, s = cos[:, None, :], sin[:, None, :]
         for li, blk in enumerate(self.blocks):
             y = F.layer_norm(x.float(), (H,), blk.n1_w.float(), blk.n1_b.float(), 1e-6).to(dt)
             qkv = _lin(y, blk.qkv_w, blk.qkv_b).view(-1, 3, nh, hd).float()
             q, k, v = qkv[:, 0], qkv[:, 1], qkv[:, 2]
-            c, s = cos[:, None, :], sin[:, None, :]
             q = q * c + torch.cat([-q[..., hd // 2:], q[..., :hd // 2]], -1) * s
             k = k * c + torch.cat([-k[..., hd // 2:], k[..., :hd // 2]], -1) * s
-            q, k, v = q.to(dt), k.to(dt), v.to(dt)
-            outs = []
-            o0 = 0
-            for n in lens:  # full attention inside each image
-                qi, ki, vi = (z[o0:o0 + n].transpose(0, 1)[None] for z in (q, k, v))
-                outs.append(F.scaled_dot_product_attention(qi, ki, vi)[0].transpose(0, 1).reshape(n, Hl))
-                o0 += n
-            x = x + self._row_parallel(torch.cat(outs), blk.proj_w, blk.proj_b)
+            x = x + self._row_parallel(attend(q.to(dt), k.to(dt), v.to(dt)), blk.proj_w, blk.proj_b)
             y = F.layer_norm(x.float(), (H,), blk.n2_w.float(), blk.n2_b.float(), 1e-6).to(dt)
             y = self._act(_lin(y, blk.fc1_w, blk.fc1_b).float()).to(dt)
             x = x + self._row_parallel(y, blk.fc2_w, blk.fc2_b)
@@ -233,6 +223,63 @@ class Qwen3VLVision(torch.nn.Module):
         emb = self._merge(self.merger, x)
         deep_t = torch.stack(deep) if deep else emb.new_zeros(0, emb.shape[0], emb.shape[1])
         return emb, deep_t
+
+    def _embed(self, pixels: torch.Tensor, grids: list[tuple[int, int, int]]):
+        """Patch embedding + interpolated position table, and the rotary tables (flat rows)."""
+        dt = self.patch_w.dtype
+        x = _lin(pixels.to(self.patch_w.device, dt), self.patch_w, self.patch_b)
+        x = x + self._pos_embed(grids)
+        cos, sin = self._rotary(grids)
+        return x, cos, sin
+
+    @torch.no_grad()
+    def forward(self, pixels: torch.Tensor, grids: list[tuple[int, int, int]]):
+        """``pixels [N, C * Tp * P * P]`` -> (embeds ``[N / merge^2, out_hidden]``, DeepStack
+        features ``[len(deepstack), N / merge^2, out_hidden]``).  Attention runs separately
+        for every frame of every image (one call per frame)."""
+        x, cos, sin = self._embed(pixels, grids)
+        frames = [h * w for t, h, w in grids for _ in range(t)]
+
+        def attend(q, k, v):
+            outs, o0 = [], 0
+            for n in frames:
+                qi, ki, vi = (z[o0:o0 + n].transpose(0, 1)[None] for z in (q, k, v))
+                outs.append(F.scaled_dot_product_attention(qi, ki, vi)[0].transpose(0, 1).reshape(n, -1))
+                o0 += n
+            return torch.cat(outs)
+
+        return self._body(x, cos, sin, attend)
+
+    def packed_body(self, xp: torch.Tensor, cp: torch.Tensor, sp: torch.Tensor,
+                    mask: torch.Tensor):
+        """Encoder over packed blocks: ``xp [B * bs, H]`` rows in ``B = mask.shape[0]`` blocks,
+        attention of all blocks in one batched call restricted by ``mask [B, 1, bs, bs]``.
+        Shapes depend on ``(B, bs)`` only, so one CUDA graph serves every plan of that size."""
+        B, bs = mask.shape[0], mask.shape[-1]
+
+        def attend(q, k, v):
+            nh, hd = q.shape[1], q.shape[2]
+            qb, kb, vb = (z.view(B, bs, nh, hd).transpose(1, 2) for z in (q, k, v))
+            o = F.scaled_dot_product_attention(qb, kb, vb, attn_mask=mask)
+            return o.transpose(1, 2).reshape(B * bs, nh * hd)
+
+        return self._body(xp, cp, sp, attend)
+
+    @torch.no_grad()
+    def forward_packed(self, pixels: torch.Tensor, grids: list[tuple[int, int, int]],
+                       plan: "VP.PackPlan", body=None):
+        """Same result as :meth:`forward` with the images' patches packed into the blocks of
+        ``plan`` (one item per image, in image order).  ``body`` replaces :meth:`packed_body`
+        (a CUDA-graph replay of it)."""
+        x, cos, sin = self._embed(pixels, grids)
+        dev = x.device
+        dst = VP.scatter_index(plan).to(dev)
+        xp, cp, sp = (VP.to_blocks(z, plan, dst) for z in (x, cos, sin))
+        lo, hi = VP.block_bounds(plan, frames=[t for t, _, _ in grids])
+        mask = VP.bounds_mask(lo.to(dev), hi.to(dev))
+        emb, deep = (body or self.packed_body)(xp, cp, sp, mask)
+        idx = VP.unpack_index(plan, self.merge ** 2).to(dev)
+        return emb.index_select(0, idx), deep.index_select(1, idx)
 
 
 def mrope_positions(prompt: list[int], image_token_id, grids: list[tuple[int, int, int]],
@@ -307,6 +354,96 @@ class Qwen3VLForConditionalGeneration(LlamaForCausalLM):
 
     vision_dp = True  # split a request's images over the TP ranks (vision data parallelism)
     vision_calls = 0  # images encoded by this rank (observability / tests)
+    vision_pack = None  # VisionConfig: images packed into blocks (None: one call per image)
+    vision_graphs = False
+    vision_blocks = 0   # packed blocks encoded by this rank
+
+    def configure_vision(self, vcfg, cuda_graphs: bool = True):
+        """Run the encoder on packed blocks of ``vcfg.vision_attention_block_size`` rows with
+        the block counts of ``vcfg.num_vision_tokens_buckets``; on the GPU (vision TP 1) each
+        block count's encoder forward is a CUDA graph captured on first use."""
+        if vcfg.vision_attention_block_size % (self.spatial_merge ** 2):
+            raise ValueError("vision_attention_block_size must be a multiple of the merge group")
+        self.vision_pack = vcfg
+        self.vision_graphs = bool(cuda_graphs and vcfg.cuda_graphs and self.device.type == "cuda"
+                                  and self.visual.tp.world == 1)
+        self._vgraphs: dict[tuple[int, int], tuple] = {}
+        self._vgraph_pool = None
+
+    def _capture_vision(self, nb: int, bs: int):
+        """CUDA graph of :meth:`Qwen3VLVision.packed_body` for ``nb`` blocks of ``bs`` rows:
+        (graph, static inputs, static outputs)."""
+        vis, dev = self.visual, self.device
+        R, hd = nb * bs, vis.hidden // vis.heads
+        ins = (torch.zeros(R, vis.hidden, dtype=vis.patch_w.dtype, device=dev),
+               torch.ones(R, hd, dtype=torch.float32, device=dev),
+               torch.zeros(R, hd, dtype=torch.float32, device=dev),
+               torch.ones(nb, 1, bs, bs, dtype=torch.bool, device=dev))
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            vis.packed_body(*ins)  # warm-up: allocator, kernel selection
+        torch.cuda.current_stream(dev).wait_stream(side)
+        if self._vgraph_pool is None:
+            self._vgraph_pool = torch.cuda.graph_pool_handle()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, pool=self._vgraph_pool):
+            outs = vis.packed_body(*ins)
+        return g, ins, outs
+
+    def _packed_runner(self, nb: int, bs: int):
+        if not self.vision_graphs:
+            return self.visual.packed_body
+        ent = self._vgraphs.get((nb, bs))
+        if ent is None:
+            ent = self._vgraphs[(nb, bs)] = self._capture_vision(nb, bs)
+        g, ins, outs = ent
+
+        def run(xp, cp, sp, mask):
+            for dst, src in zip(ins, (xp, cp, sp, mask)):
+                dst.copy_(src)
+            g.replay()
+            return outs
+        return run
+
+    def _encode_packed(self, pixels: torch.Tensor, grids: list[tuple[int, int, int]]):
+        """:meth:`encode_images` on packed blocks.  With vision data parallelism the block count
+        is padded to the ``W`` replicas, replica ``r`` encodes blocks ``[r * nb, (r + 1) * nb)``
+        and the merged rows are all-gathered before they are put back in image order.
+        Returns None when an image does not fit a block (the caller encodes per image)."""
+        vis, vc = self.visual, self.vision_pack
+        V = vis.tp.world
+        W = self.tp.world // V if self.vision_dp else 1
+        bs = vc.vision_attention_block_size
+        sizes = [t * h * w for t, h, w in grids]
+        if max(sizes) > bs:
+            return None
+        try:
+            plan = VP.plan_for_buckets(sizes, bs, vc.num_vision_tokens_buckets, dp=W)
+        except ValueError:  # more tokens than the largest bucket: the minimal plan, uncaptured
+            plan = VP.plan_for_buckets(sizes, bs, None, dp=W)
+        x, cos, sin = vis._embed(pixels, grids)
+        dev = x.device
+        dst = VP.scatter_index(plan).to(dev)
+        lo, hi = VP.block_bounds(plan, frames=[t for t, _, _ in grids])
+        nb = plan.num_blocks // W
+        r = self.tp.rank // V if W > 1 else 0
+        rows = slice(r * nb * bs, (r + 1) * nb * bs)
+        xp, cp, sp = (VP.to_blocks(z, plan, dst)[rows] for z in (x, cos, sin))
+        mask = VP.bounds_mask(lo[r * nb:(r + 1) * nb].to(dev), hi[r * nb:(r + 1) * nb].to(dev))
+        emb, deep = self._packed_runner(nb, bs)(xp, cp, sp, mask)
+        self.vision_blocks += nb
+        H, nd = self.H, len(vis.deep_idx)
+        if W > 1:
+            n = emb.shape[0]
+            parts = [emb] + ([deep.permute(1, 0, 2).reshape(n, nd * H)] if nd else [])
+            allp = self.tp.all_gather(torch.cat(parts, 1).unsqueeze(0), dim=0)  # [W * V, n, .]
+            allp = allp.view(W, V, n, -1)[:, 0].reshape(W * n, -1)  # each replica's first rank
+            emb = allp[:, :H]
+            deep = (allp[:, H:].reshape(W * n, nd, H).permute(1, 0, 2) if nd
+                    else emb.new_zeros(0, W * n, H))
+        idx = VP.unpack_index(plan, self.spatial_merge ** 2).to(dev)
+        return emb.index_select(0, idx), deep.index_select(1, idx).contiguous()
 
     def encode_images(self, pixels: torch.Tensor, grids: list[tuple[int, int, int]]):
         """Merged vision embeddings ``[tokens, H]`` and DeepStack features ``[n_deep, tokens, H]``
@@ -317,6 +454,11 @@ class Qwen3VLForConditionalGeneration(LlamaForCausalLM):
         (padded to the largest share), instead of every rank encoding every image.  Reference:
         the vision TP/DP groups (vllm_neuron/parallel/neuron_parallel_state.py:667-701; vision
         DP defaults to the world, vllm_neuron/model/neuron_config.py:345-404)."""
+        if self.vision_pack is not None:
+            res = self._encode_packed(pixels, grids)
+            if res is not None:
+                self.vision_calls += len(grids)
+                return res
         V = self.visual.tp.world
         W = self.tp.world // V   # vision-DP replicas of V consecutive ranks
         if W == 1 or len(grids) < 2 or not self.vision_dp:

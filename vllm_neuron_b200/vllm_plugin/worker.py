@@ -128,11 +128,13 @@ class B200Worker(WorkerBase):
             if backend == "nccl":
                 kw["device_id"] = self.device
             dist.init_process_group(**kw)
+        from ..config import vision_tp_of
+
         ac = dict(self.vllm_config.additional_config or {})
         opts = ac.get("neuron_config") or ac.get("b200_config") or {}
         ps.initialize_parallel_state(ps.ParallelConfig(world_size=world,
                                                        tensor_parallel_size=par.tensor_parallel_size,
-                                                       vision_tp_size=int(opts.get("vision_tp_size", 1))))
+                                                       vision_tp_size=vision_tp_of(ac)))
 
     def _engine_args(self, load_dummy: bool) -> EngineArgs:
         mc, sc, cc = self.model_config, self.scheduler_config, self.cache_config
