@@ -149,7 +149,8 @@ def bench_gemms_fp8(tp: int):
 def bench_gemms_fp8_block(tp: int):
     """128 x 128 block-FP8 weights (Llama-3-70B shapes per TP shard): W8A16 (weights widened to
     bf16 in shared memory) against W8A8 (1 x 128 fp8 activation blocks, per-k-block promotion),
-    activation quantization included; bytes count the fp8 weight."""
+    activation quantization included; bytes count the fp8 weight.  Also MXFP8 (e8m0 scale per 32
+    elements, hardware block scaling) and the bf16-weight GEMM of the same shape."""
     H, I, Hq, Hkv, D = 8192, 28672, 64, 8, 128
     shapes = {"qkv": ((Hq + 2 * Hkv) * D // tp, H), "o_proj": (H, Hq * D // tp),
               "gate_up": (2 * I // tp, H), "down": (H, I // tp)}
@@ -179,10 +180,22 @@ def bench_gemms_fp8_block(tp: int):
                     sp = L.pick_splits(N, K, L.num_sms(x.device), 128) if tiles < L.num_sms(x.device) else -1
                     ext().gemm_fp8_block(bw.q, xq, acc, L.skinny_bn(M), sp, bw.scales, xs)
                 t["fp8"] = timeit(w8a8_direct)
+            # MXFP8 (per-32 e8m0 scales) on the block-scaled MMA, activation quantization included,
+            # and the bf16-weight GEMM of the same shape for context
+            mw = L.MXFP8Weight.from_weight(bw.dequant_bf16_ref())
+            wb = bw.dequant_bf16_ref()
+            if M > L.SKINNY_MAX:
+                t["mx8"] = timeit(lambda: L.gemm_out(x, mw, out))
+                t["w16"] = timeit(lambda: L.gemm_out(x, wb, out))
+            else:
+                t["mx8"] = timeit(lambda: L.gemm_accumulate(x, mw, acc))
+                t["w16"] = timeit(lambda: L.gemm_accumulate(x, wb, acc))
             rows.append({"op": f"gemm_fp8_block_{name}", "M": M, "N": N, "K": K,
                          "w8a16_ms": t["bf16"], "w8a8_ms": t["fp8"],
                          "w8a8_tflops": 2.0 * M * N * K / t["fp8"] / 1e9,
-                         "w8a8_weight_gbs": N * K / t["fp8"] / 1e6, "speedup": t["bf16"] / t["fp8"]})
+                         "w8a8_weight_gbs": N * K / t["fp8"] / 1e6, "speedup": t["bf16"] / t["fp8"],
+                         "mx8_ms": t["mx8"], "mx8_tflops": 2.0 * M * N * K / t["mx8"] / 1e9,
+                         "mx8_weight_gbs": N * K / t["mx8"] / 1e6, "bf16_weights_ms": t["w16"]})
             print(json.dumps(rows[-1]), flush=True)
     return rows
 
@@ -338,6 +351,8 @@ def profile_case(name: str):
     fmha       tcgen05 prefill attention, 2 x 4096 tokens, Llama-3-8B heads (fmha_prefill_kernel)
     gemm2sm    gate/up + SwiGLU projection, M = 8192, N = 28672, K = 4096 (gemm2sm_kernel)
     gemm_dec   decode gate/up projection, M = 64, stream-K fp32 reduction (gemm_bf16_kernel)
+    mx8_dec    MXFP8 decode gate/up, Llama-3-70B TP2 shard (N = 28672, K = 8192), M = 64
+    mx8_pre    MXFP8 prefill gate/up, same shard, M = 4096 (bf16 store)
     """
     if name == "fmha":
         Hq, Hkv, D, bs, B, S = 32, 8, 128, 16, 2, 4096
@@ -365,6 +380,16 @@ def profile_case(name: str):
         w = torch.randn(28672, 4096, device="cuda", dtype=torch.bfloat16) * 0.02
         acc = torch.zeros(64, 28672, device="cuda", dtype=torch.float32)
         fn = lambda: L.gemm_accumulate(x, w, acc)
+    elif name in ("mx8_dec", "mx8_pre"):
+        M = 64 if name == "mx8_dec" else 4096
+        x = torch.randn(M, 8192, device="cuda", dtype=torch.bfloat16)
+        mw = L.MXFP8Weight.from_weight(torch.randn(28672, 8192, device="cuda", dtype=torch.bfloat16) * 0.02)
+        if M <= L.SKINNY_MAX:
+            acc = torch.zeros(M, 28672, device="cuda", dtype=torch.float32)
+            fn = lambda: L.gemm_accumulate(x, mw, acc)
+        else:
+            out = torch.empty(M, 28672, device="cuda", dtype=torch.bfloat16)
+            fn = lambda: L.gemm_out(x, mw, out)
     else:
         raise SystemExit(f"unknown profile case {name}")
     for _ in range(3):
@@ -375,7 +400,7 @@ def profile_case(name: str):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--profile-case", type=str, default=None, help="fmha | gemm2sm | gemm_dec (see profile_case)")
+    ap.add_argument("--profile-case", type=str, default=None, help="fmha | gemm2sm | gemm_dec | mx8_dec | mx8_pre (see profile_case)")
     ap.add_argument("--tp", type=int, default=1)
     ap.add_argument("--json", type=str, default=None)
     ap.add_argument("--only", type=str, default="gemm,decode,prefill,moe,deltanet")

@@ -77,9 +77,10 @@ def main():
     ap.add_argument("--max-num-batched-tokens", type=int, default=None)
     ap.add_argument("--warmup-prompts", type=int, default=4)
     ap.add_argument("--json", default=None)
-    ap.add_argument("--quant", default="auto", choices=["auto", "none", "fp8_static", "fp8_block"],
+    ap.add_argument("--quant", default="auto", choices=["auto", "none", "fp8_static", "fp8_block", "mxfp8"],
                     help="fp8_static: W8A8 FP8 projections (random weights quantized per tensor); "
-                         "fp8_block: 128 x 128 block-scaled FP8 weights, bf16 activations; auto: the "
+                         "fp8_block: 128 x 128 block-scaled FP8 weights, bf16 activations; mxfp8: "
+                         "MXFP8 projections (e8m0 scale per 32, block-scaled tensor cores); auto: the "
                          "configuration's own (fp8_block for llama3-70b and qwen3.6-a3b)")
     ap.add_argument("--sp", action="store_true", help="sequence-parallel prefill (TP > 1)")
     ap.add_argument("--fp8-block-act", choices=["fp8", "bf16"], default=None,
@@ -147,7 +148,8 @@ def main():
            "dtype": "bf16" + ({"fp8_static": " activations, fp8 W8A8 projections",
                                "fp8_block": (" activations, 128x128 block-scaled fp8 weights (decode: "
                                              + ("W8A16" if a.fp8_block_act == "bf16" else
-                                                "W8A8, 1x128 fp8 activation blocks") + ")")}.get(quant, "")),
+                                                "W8A8, 1x128 fp8 activation blocks") + ")"),
+                               "mxfp8": " activations, MXFP8 W8A8 projections (e4m3, e8m0 per 32)"}.get(quant, "")),
            "sp": bool(nc.get("sequence_parallel")), "max_num_batched_tokens": mnbt,
            "build": "nccl+cublas baseline" if a.baseline else "fused sm_100a",
            "data": "synthetic prompts, random-init weights"}

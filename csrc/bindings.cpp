@@ -263,6 +263,68 @@ void gemm_fp8_block(const at::Tensor& w, const at::Tensor& xq, at::Tensor& out, 
   check_launch("gemm_fp8_block");
 }
 
+// MXFP8 activations: x bf16 [M, K] -> q e4m3 [M, K] and e8m0 scales in 512-byte atoms
+// [ceil(M / 128), K / 128, 512] (rows >= M of the last atom are left as they are).
+void quant_mx8(const at::Tensor& x, at::Tensor& q, at::Tensor& sf) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  TORCH_CHECK(q.scalar_type() == at::kFloat8_e4m3fn && sf.scalar_type() == at::kByte, "quant_mx8: q e4m3, sf uint8");
+  TORCH_CHECK(x.dim() == 2 && q.dim() == 2 && x.stride(1) == 1 && q.stride(1) == 1 && sf.is_contiguous(),
+              "quant_mx8: contiguous rows");
+  const int64_t M = x.size(0), K = x.size(1);
+  TORCH_CHECK(q.size(0) >= M && q.size(1) == K && sf.numel() >= ((M + 127) / 128) * (K / 128) * 512,
+              "quant_mx8: output shapes");
+  const c10::cuda::CUDAGuard guard(x.device());
+  b200::quant_mx8_launch(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0),
+                         reinterpret_cast<uint8_t*>(q.data_ptr()), q.stride(0), sf.data_ptr<uint8_t>(), (int)M,
+                         (int)K, cur_stream());
+  check_launch("quant_mx8");
+}
+
+// MXFP8 x MXFP8 GEMM on the block-scaled tensor cores: out = a @ b^T with a [M, K], b [N, K] e4m3
+// and their scale atoms (see quant_mx8).  epi: EPI_BF16 (bn 128, bf16 out[M, N]), EPI_BF16_T
+// (bf16 out[N, M]), EPI_F32_RED_T (fp32 out[N, M] +=, split-K) or EPI_F32_RED (fp32 out[M, N] +=).
+void gemm_mx8(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, int64_t epi, int64_t bn,
+              int64_t splits, const at::Tensor& sfa, const at::Tensor& sfb) {
+  CHECK_CUDA(a);
+  CHECK_CUDA(b);
+  TORCH_CHECK(a.scalar_type() == at::kFloat8_e4m3fn && b.scalar_type() == at::kFloat8_e4m3fn,
+              "gemm_mx8: operands must be float8_e4m3fn");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.size(1) == b.size(1), "gemm_mx8: bad shapes");
+  TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1 && out.stride(1) == 1, "gemm_mx8: inner dims");
+  TORCH_CHECK(sfa.scalar_type() == at::kByte && sfb.scalar_type() == at::kByte && sfa.is_contiguous() &&
+                  sfb.is_contiguous(), "gemm_mx8: scale atoms must be contiguous uint8");
+  const int64_t M = a.size(0), N = b.size(0), K = a.size(1);
+  TORCH_CHECK(K % 128 == 0 && sfa.numel() >= ((M + 127) / 128) * (K / 128) * 512 &&
+                  sfb.numel() >= ((N + 127) / 128) * (K / 128) * 512, "gemm_mx8: scale atoms do not cover the operands");
+  const bool f32 = epi == b200::EPI_F32_RED_T || epi == b200::EPI_F32_RED;
+  TORCH_CHECK(out.scalar_type() == (f32 ? at::kFloat : at::kBFloat16), "gemm_mx8: output dtype");
+  const bool tr = epi == b200::EPI_F32_RED_T || epi == b200::EPI_BF16_T;
+  TORCH_CHECK(out.size(0) >= (tr ? N : M) && out.size(1) == (tr ? M : N), "gemm_mx8: output shape");
+  const c10::cuda::CUDAGuard guard(a.device());
+  b200::GemmArgs g{};
+  g.A = a.data_ptr();
+  g.B = b.data_ptr();
+  g.out = out.data_ptr();
+  g.lda = a.stride(0);
+  g.ldb = b.stride(0);
+  g.ldo = out.stride(0);
+  g.M = (int)M;
+  g.N = (int)N;
+  g.K = (int)K;
+  g.bn = (int)bn;
+  g.epi = (int)epi;
+  g.splits = (int)splits;
+  g.status = status_word();
+  g.fp8 = 1;
+  g.w8 = 6;
+  g.sfa = sfa.data_ptr<uint8_t>();
+  g.sfb = sfb.data_ptr<uint8_t>();
+  if (M == 0 || N == 0) return;
+  b200::gemm_bf16_launch(g, cur_stream());
+  check_launch("gemm_mx8");
+}
+
 // Block-scaled FP8 W8A8 prefill GEMM: out[m, n] = sum_k xq[m, k] w[n, k] * xs[m, k / 128] *
 // ws[n / 128, k / 128] (bf16 store; tokens as the 128-row operand, 128-wide weight tiles).
 void gemm_fp8_block_prefill(const at::Tensor& xq, const at::Tensor& w, at::Tensor& out,
@@ -1198,6 +1260,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_fp8_block", &gemm_fp8_block);
   m.def("gemm_fp8_block_prefill", &gemm_fp8_block_prefill);
   m.def("quant_fp8_block", &quant_fp8_block);
+  m.def("quant_mx8", &quant_mx8);
+  m.def("gemm_mx8", &gemm_mx8);
   m.def("quant_fp8", &quant_fp8);
   m.def("rmsnorm_quant", &rmsnorm_quant);
   m.def("sp_norm_push", &sp_norm_push);

@@ -242,6 +242,28 @@ __device__ __forceinline__ void umma_f8_ss(uint32_t d_tmem, uint64_t a_desc, uin
       : "memory");
 }
 
+// Block-scaled e4m3 x e4m3 (MXFP8): kind::mxf8f6f4 with one e8m0 scale per 32 k elements of
+// every A row and B row, read from TMEM at `sfa_tmem` / `sfb_tmem` (their top two bits select
+// the byte of the 32-bit scale word, as the instruction descriptor's scale-factor ids do).
+// K = 32 elements per instruction.
+__device__ __forceinline__ void umma_mx8_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t sfa_tmem, uint32_t sfb_tmem,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+
+// Shared memory -> TMEM copy of a 32-row x 16-byte matrix (described by an unswizzled smem
+// descriptor) into 4 columns of lanes 0..31, replicated into all four lane quarters.  Ordered
+// with the tcgen05.mma issued after it by the same thread.
+__device__ __forceinline__ void tmem_cp_32x128b_warpx4(uint32_t taddr, uint64_t s_desc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(s_desc)
+               : "memory");
+}
+
 // D[tmem] (+)= A[tmem] * B[smem desc]^T, kind::f16 (A operand from TMEM).
 __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
                                             uint32_t idesc, uint32_t accumulate) {
@@ -322,6 +344,24 @@ __device__ __forceinline__ uint64_t make_sdesc_sw128(uint32_t smem_addr) {
   d |= (uint64_t)1 << 46;             // version
   d |= (uint64_t)2 << 61;             // SWIZZLE_128B
   return d;
+}
+
+// Unswizzled (interleaved) K-major descriptor: 8-row core matrices of 16-byte rows, core
+// matrices `sbo` bytes apart along the rows and `lbo` bytes apart along K.
+__device__ __forceinline__ uint64_t make_sdesc_none(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;  // version; layout type 0 = no swizzle
+  return d;
+}
+
+// Instruction descriptor of the block-scaled kinds (kind::mxf8f6f4 here): A and B e4m3 (format
+// 0), both K-major, e8m0 scales (bit 23), fp32 accumulation implied; the scale-factor ids
+// (bits 4-5 for B, 29-30 for A) are or-ed in per instruction.
+__host__ __device__ constexpr uint32_t make_idesc_mx8(int M, int N) {
+  return ((uint32_t)(N >> 3) << 17) | (1u << 23) | ((uint32_t)(M >> 4) << 24);
 }
 
 // Instruction descriptor for kind::f16 with fp32 accumulation, both operands K-major.

@@ -78,6 +78,11 @@ struct GemmArgs {
   // (per-k-block promotion), so no operand is widened.
   const float* x_scales = nullptr;
   int x_scale_ld = 0;
+  // MXFP8 x MXFP8 (w8 = 6, fp8 = 1): e4m3 A and B with e8m0 scales per 32 k elements in the
+  // 512-byte atom layout (atom (row / 128, k / 128) at ((row / 128) * K / 128 + k / 128) * 512;
+  // row r's 4 scales of the atom at (r % 32) * 16 + ((r / 32) % 4) * 4); K a multiple of 128.
+  const uint8_t* sfa = nullptr;
+  const uint8_t* sfb = nullptr;
 };
 
 void gemm_bf16_launch(const GemmArgs& args, cudaStream_t stream);

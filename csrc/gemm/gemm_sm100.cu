@@ -92,6 +92,12 @@ struct GemmParams {
   const uint8_t* wsc8;  // MXFP4: e8m0 scale bytes [wsc_rows][wsc_ld], one per 32 elements
   const float* xsc;     // W8 = 5: activation scales [tokens][xsc_ld], one per 128-wide k block
   int xsc_ld;
+  // W8 = 6 (MXFP8): e8m0 scales of A and B in 512-byte atoms, atom (row block, k block) at
+  // ((row / 128) * sf_kb + k / 128) * 512; inside an atom, the 4 scales of row r (32 k
+  // elements each) are bytes (r % 32) * 16 + ((r / 32) % 4) * 4 + [0, 4)
+  const uint8_t* sfa;
+  const uint8_t* sfb;
+  int sf_kb;
 };
 
 // Bounded wait until a monotonic counter (written by a peer with a system-scope release)
@@ -210,6 +216,10 @@ struct SegCursor {
 };
 
 
+__host__ __device__ constexpr uint32_t tmem_cols_pow2(int n) {
+  return n <= 32 ? 32u : n <= 64 ? 64u : n <= 128 ? 128u : n <= 256 ? 256u : 512u;
+}
+
 template <int BN>
 struct TmemCols {
   static constexpr int v = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128
@@ -244,6 +254,11 @@ __device__ __forceinline__ void fp4x8_to_f16x8_gemm(uint32_t w, uint32_t (&o)[4]
 // W8 = 3 / 4: the same for an MXFP4 weight on A / B (GPT-OSS experts): 32 packed bytes per row
 // per stage (two e2m1 per byte), widened with the hardware e2m1x2 conversion and the e8m0
 // scale of each 32-element block -- half a byte per element from HBM.
+// W8 = 6 (MXFP8 x MXFP8, FP8 operands): the native block-scaled MMA.  Each stage also carries the
+// 512-byte e8m0 scale atoms of its A and B rows (1D bulk copies on the stage's barrier); the MMA
+// thread copies them into TMEM (tcgen05.cp 32x128b.warpx4, a fresh 8-column slot per stage)
+// and issues kind::mxf8f6f4.block_scale with the scale byte of each 32-element k step, so the
+// hardware applies the per-32 scales and the epilogue is the plain fp32 one.
 template <int BN, int STAGES, int EPI, bool FP8 = false, int W8 = 0>
 __global__ void __launch_bounds__((W8 >= 1 && W8 <= 4) ? 320 : 192, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA,
@@ -255,20 +270,29 @@ __global__ void __launch_bounds__((W8 >= 1 && W8 <= 4) ? 320 : 192, 1)
                 "promotion mode: FP8 operands; swapped decode layout with N tile <= 64, or tokens as A "
                 "with a 128-wide weight tile");
   constexpr bool kFP4 = W8 == 3 || W8 == 4;                  // MXFP4 (else block FP8)
+  constexpr bool kMX = W8 == 6;                              // MXFP8, hardware block scaling
+  static_assert(!kMX || (FP8 && BN <= 128 && EPI != EPI_SILU_BF16 && EPI != EPI_BF16_RS),
+                "MXFP8 mode: e4m3 operands, N tile <= 128, plain epilogues");
+  constexpr int kSFBytes = kMX ? 1024 : 0;                    // scale atoms of A and B per stage
   constexpr int kWSide = !kConv ? 0 : (W8 == 1 || W8 == 3) ? 1 : 2;  // weight operand: A / B
   constexpr int kW8Rows = kWSide == 1 ? kBM : kWSide == 2 ? BN : 0;  // weight rows per tile
   constexpr int kSRow = kFP4 ? kBK / 2 : kBK;                 // staged bytes per row per stage
   constexpr int kSBytes = kW8Rows * kSRow;                    // staging bytes per stage
-  constexpr int kStageBytes = kATileBytes + kBTileBytes + kSBytes;
+  constexpr int kStageBytes = kATileBytes + kBTileBytes + kSBytes + kSFBytes;
   // bytes the TMA delivers per stage (the converted operand is written by the converter)
   constexpr int kStageTx = kWSide == 1   ? kSBytes + kBTileBytes
                            : kWSide == 2 ? kATileBytes + kSBytes
-                                         : kATileBytes + kBTileBytes;
+                                         : kATileBytes + kBTileBytes + kSFBytes;
   // accumulator buffers: 2 tiles in flight; the promotion mode keeps 4 k-block accumulators so
   // the MMA issuer runs up to 4 k blocks ahead of the promoting epilogue
   constexpr int kAccBufs = kPromote ? 4 : 2;
-  constexpr uint32_t kTmemCols = kPromote ? TmemCols<2 * BN>::v : TmemCols<BN>::v;
-  constexpr uint32_t kIdesc = make_idesc_f16(kBM, BN, !FP8);  // FP8: type fields 0 = E4M3
+  constexpr int kSFCol0 = 2 * BN;  // MXFP8: scale slots (8 columns per stage) after the accumulators
+  constexpr uint32_t kTmemCols = kPromote ? TmemCols<2 * BN>::v
+                                 : kMX    ? tmem_cols_pow2(kSFCol0 + 8 * STAGES)
+                                          : TmemCols<BN>::v;
+  static_assert(!kMX || kSFCol0 + 8 * STAGES <= 512, "MXFP8 TMEM budget");
+  constexpr uint32_t kIdesc = kMX ? make_idesc_mx8(kBM, BN)
+                                  : make_idesc_f16(kBM, BN, !FP8);  // FP8: type fields 0 = E4M3
   constexpr int kKElems = FP8 ? 2 * kBK : kBK;                  // elements per k-block
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -278,6 +302,7 @@ __global__ void __launch_bounds__((W8 >= 1 && W8 <= 4) ? 320 : 192, 1)
   uint8_t* smA = smem;
   uint8_t* smB = smem + STAGES * kATileBytes;
   uint8_t* smS = smB + STAGES * kBTileBytes;  // fp8 weight staging (W8)
+  uint8_t* smSF = smS + STAGES * kSBytes;     // MXFP8 scale atoms: [A 512 | B 512] per stage
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * kStageBytes);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* conv_bar = empty_bar + STAGES;  // converted operand ready (W8)
@@ -344,11 +369,17 @@ __global__ void __launch_bounds__((W8 >= 1 && W8 <= 4) ? 320 : 192, 1)
         }
         uint8_t* dst = kWSide == 1 ? smS + s * kSBytes : smA + s * kATileBytes;
         tma_load_2d(&tmA, &full_bar[s], dst, (kFP4 && kWSide == 1) ? kb * kSRow : kb * kKElems, a_row, hint_a);
+        if constexpr (kMX)
+          bulk_load_1d(smSF + s * kSFBytes, p.sfa + ((long long)(a_row >> 7) * p.sf_kb + kb) * 512, 512,
+                       &full_bar[s], hint_a);
       };
       auto load_b = [&](int s, int kb, int nb, int mb) {
         const int row = p.grouped == 2 ? p.gtiles[mb].y : (p.grouped ? tile_rows(p, mb).b_base : 0) + nb * BN;
         uint8_t* dst = kWSide == 2 ? smS + s * kSBytes : smB + s * kBTileBytes;
         tma_load_2d(&tmB, &full_bar[s], dst, (kFP4 && kWSide == 2) ? kb * kSRow : kb * kKElems, row, hint_b);
+        if constexpr (kMX)
+          bulk_load_1d(smSF + s * kSFBytes + 512, p.sfb + ((long long)(row >> 7) * p.sf_kb + kb) * 512, 512,
+                       &full_bar[s], hint_b);
       };
       // The grouped tile list is written by the previous kernel.
       if (p.grouped) pdl_wait();
@@ -452,6 +483,28 @@ __global__ void __launch_bounds__((W8 >= 1 && W8 <= 4) ? 320 : 192, 1)
           tc_fence_after();
           const uint32_t a_addr = smem_u32(smA + s * kATileBytes);
           const uint32_t b_addr = smem_u32(smB + s * kBTileBytes);
+          if constexpr (kMX) {
+            // this stage's scale atoms -> its TMEM slot (A: 4 columns, B: 4 columns), then the
+            // four 32-element k steps, step k reading byte k of each scale word
+            const uint32_t sf_a = tmem_base + kSFCol0 + s * 8;
+            const uint32_t sf_b = sf_a + 4;
+            const uint32_t sf_src = smem_u32(smSF + s * kSFBytes);
+            tmem_cp_32x128b_warpx4(sf_a, make_sdesc_none(sf_src, 128, 128));
+            tmem_cp_32x128b_warpx4(sf_b, make_sdesc_none(sf_src + 512, 128, 128));
+            // B rows of this tile start (nb * BN) % 128 rows into their atom: 32 rows per column
+            const uint32_t b_col = (uint32_t)(((nb * BN) & 127) >> 5);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const uint64_t adesc = make_sdesc_sw128(a_addr + k * 32);
+              const uint64_t bdesc = make_sdesc_sw128(b_addr + k * 32);
+              const uint32_t accum = (kb > k0 || k > 0) ? 1u : 0u;
+              const uint32_t id = (uint32_t)k;
+              umma_mx8_ss(d_tmem, adesc, bdesc, kIdesc | (id << 4) | (id << 29), sf_a | (id << 30),
+                          (sf_b + b_col) | (id << 30), accum);
+            }
+            umma_commit(&empty_bar[s]);
+            continue;
+          }
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k) {
             const uint64_t adesc = make_sdesc_sw128(a_addr + k * 32);
@@ -891,7 +944,7 @@ static void launch_impl(const CUtensorMap& ta, const CUtensorMap& tb, const Gemm
                         int grid, cudaStream_t stream) {
   constexpr int w8_rows = (W8 == 1 || W8 == 3) ? kBM : (W8 == 2 || W8 == 4) ? BN : 0;
   constexpr int srow = (W8 == 3 || W8 == 4) ? kBK / 2 : kBK;
-  constexpr int smem = STAGES * (kATileBytes + BN * kBK * 2 + w8_rows * srow) + 1024 + 512;
+  constexpr int smem = STAGES * (kATileBytes + BN * kBK * 2 + w8_rows * srow + (W8 == 6 ? 1024 : 0)) + 1024 + 512;
   static_assert(smem <= 232448, "shared memory budget");
   auto kern = gemm_bf16_kernel<BN, STAGES, EPI, FP8, W8>;
   static std::atomic<uint64_t> configured{0};  // per instantiation, per device
@@ -959,8 +1012,17 @@ void gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
       throw std::invalid_argument("gemm: block-scaled FP8 W8A8 needs e4m3 operands, weight and activation "
                                   "block scales, EPI_F32_RED_T (weights as A) or EPI_BF16 with bn 128 "
                                   "(weights as B), K and weight rows in 128s");
+  } else if (a.w8 == 6) {
+    const bool ok_epi = (a.epi == EPI_BF16 && a.bn == 128) || a.epi == EPI_BF16_T || a.epi == EPI_F32_RED_T ||
+                        (a.epi == EPI_F32_RED && a.bn == 128);
+    if (!a.fp8 || a.sfa == nullptr || a.sfb == nullptr || grouped || a.sp != nullptr || a.K % 128 != 0 ||
+        !ok_epi || (a.bn != 16 && a.bn != 32 && a.bn != 64 && a.bn != 128) || (a.bn == 16 && a.N > 16) ||
+        (a.epi == EPI_BF16_T && a.bn == 128))
+      throw std::invalid_argument("gemm: MXFP8 needs e4m3 operands with both scale atoms, K in 128s, N tile "
+                                  "16 (N <= 16) / 32 / 64 / 128 and EPI_BF16 (bn 128), EPI_BF16_T, "
+                                  "EPI_F32_RED_T or EPI_F32_RED");
   } else if (a.w8 != 0) {
-    throw std::invalid_argument("gemm: w8 must be 0..5");
+    throw std::invalid_argument("gemm: w8 must be 0..6");
   }
   // block-FP8 weight operand: bytes, 64 per row per stage, no swizzle (the converter swizzles)
   const CUtensorMap ta = a.w8 == 3 ? make_tmap_u8_2d(a.A, a.K / 2, a_rows, a.lda, kBK / 2, kBM, 0)
@@ -989,6 +1051,9 @@ void gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
   p.wsc8 = a.w_scales8;
   p.xsc = a.x_scales;
   p.xsc_ld = a.x_scale_ld;
+  p.sfa = a.sfa;
+  p.sfb = a.sfb;
+  p.sf_kb = a.K / 128;
   p.streamk = a.splits < 0 ? 1 : 0;
   int splits = a.splits < 1 ? 1 : a.splits;
   if (splits > p.num_k_blocks) splits = p.num_k_blocks;
@@ -1028,6 +1093,21 @@ void gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
   if (bn == BN_ && a.epi == EPI_) {                                       \
     launch_impl<BN_, ST_, EPI_, true>(ta, tb, p, grid, stream);           \
     return;                                                               \
+  }
+  if (a.fp8 && a.w8 == 6) {
+    if (a.epi == EPI_BF16) { launch_impl<128, 6, EPI_BF16, true, 6>(ta, tb, p, grid, stream); return; }
+    if (a.epi == EPI_F32_RED) { launch_impl<128, 6, EPI_F32_RED, true, 6>(ta, tb, p, grid, stream); return; }
+    if (a.epi == EPI_F32_RED_T) {
+      if (bn == 16) { launch_impl<16, 8, EPI_F32_RED_T, true, 6>(ta, tb, p, grid, stream); return; }
+      if (bn == 32) { launch_impl<32, 8, EPI_F32_RED_T, true, 6>(ta, tb, p, grid, stream); return; }
+      if (bn == 64) { launch_impl<64, 8, EPI_F32_RED_T, true, 6>(ta, tb, p, grid, stream); return; }
+      launch_impl<128, 6, EPI_F32_RED_T, true, 6>(ta, tb, p, grid, stream);
+      return;
+    }
+    if (bn == 16) { launch_impl<16, 8, EPI_BF16_T, true, 6>(ta, tb, p, grid, stream); return; }
+    if (bn == 32) { launch_impl<32, 8, EPI_BF16_T, true, 6>(ta, tb, p, grid, stream); return; }
+    launch_impl<64, 8, EPI_BF16_T, true, 6>(ta, tb, p, grid, stream);
+    return;
   }
   if (a.fp8 && a.w8 == 5) {
     if (a.epi == EPI_BF16) { launch_impl<128, 6, EPI_BF16, true, 5>(ta, tb, p, grid, stream); return; }

@@ -52,6 +52,8 @@ void rope_kv_write_launch(const RopeKvParams& p, void* qkv, bool qkv_is_f32, int
 void quant_fp8_launch(const __nv_bfloat16* x, long long ldx, uint8_t* out, long long ldo, int rows,
                       int cols, float inv_scale, cudaStream_t stream);
 // Per-token, per-128-column dynamic quantization (scales [rows][lds], max|x| / 448).
+void quant_mx8_launch(const __nv_bfloat16* x, long long ldx, uint8_t* out, long long ldo, uint8_t* sf,
+                      int rows, int cols, cudaStream_t stream);
 void quant_fp8_block_launch(const __nv_bfloat16* x, long long ldx, uint8_t* out, long long ldo,
                             float* scales, int lds, int rows, int cols, cudaStream_t stream);
 // row_scales == null: static per-tensor scale; else per-row dynamic scales (max|y| / 448).

@@ -155,6 +155,49 @@ void quant_fp8_block_launch(const __nv_bfloat16* x, long long ldx, uint8_t* out,
              scales, lds, nblk);
 }
 
+// MXFP8 quantization (OCP microscaling, e4m3 elements, e8m0 scale per 32 elements): one warp per
+// (row, 128-column block), 8 lanes per 32-element group.  The group's scale is the smallest
+// power of two 2^e with max|x| <= 448 * 2^e, so the scaled values never saturate and
+// q = rn_e4m3(x * 2^-e) is an exact power-of-two scaling before the rounding.  Scales go into
+// the 512-byte atom layout the block-scaled GEMM reads: atom (row / 128, block) holds, for row r,
+// its 4 group scales at (r % 32) * 16 + ((r / 32) % 4) * 4.
+__global__ void __launch_bounds__(256) quant_mx8_kernel(const __nv_bfloat16* __restrict__ x, long long ldx,
+                                                        uint8_t* __restrict__ out, long long ldo,
+                                                        uint8_t* __restrict__ sf, int nblk) {
+  pdl_trigger();
+  pdl_wait();
+  const long long r = blockIdx.x;
+  const int b = blockIdx.y * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (b >= nblk) return;
+  const int c = b * 128 + lane * 4;
+  const uint2 v = *reinterpret_cast<const uint2*>(x + r * ldx + c);
+  const float2 a = unpack_bf16x2(v.x), d = unpack_bf16x2(v.y);
+  float m = fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(d.x), fabsf(d.y)));
+#pragma unroll
+  for (int o = 1; o < 8; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  // m = 1.f * 2^(E - 127): m <= 1.75 * 2^(8 + e) <=> e >= E - 135 (+1 when 1.f > 1.75)
+  const uint32_t bits = __float_as_uint(m);
+  int e = (int)((bits >> 23) & 0xffu) - 135 + ((bits & 0x7fffffu) > 0x600000u ? 1 : 0);
+  if (m == 0.f) e = 0;
+  e = max(-127, min(127, e));
+  const float inv = e >= 127 ? __uint_as_float(0x00400000u) : __uint_as_float((uint32_t)(127 - e) << 23);
+  *reinterpret_cast<uint32_t*>(out + r * ldo + c) = q4(a.x * inv, a.y * inv, d.x * inv, d.y * inv);
+  if ((lane & 7) == 0) {
+    const int ri = (int)(r & 127);
+    sf[((r >> 7) * nblk + b) * 512 + (ri & 31) * 16 + (ri >> 5) * 4 + (lane >> 3)] = (uint8_t)(e + 127);
+  }
+}
+
+void quant_mx8_launch(const __nv_bfloat16* x, long long ldx, uint8_t* out, long long ldo, uint8_t* sf,
+                      int rows, int cols, cudaStream_t stream) {
+  if (rows == 0) return;
+  if (cols % 128 != 0 || ldx % 4 != 0 || ldo % 4 != 0)
+    throw std::invalid_argument("quant_mx8: columns must be a multiple of 128");
+  const int nblk = cols / 128;
+  launch_pdl(quant_mx8_kernel, dim3(rows, (nblk + 7) / 8), dim3(256), 0, stream, x, ldx, out, ldo, sf, nblk);
+}
+
 void quant_fp8_launch(const __nv_bfloat16* x, long long ldx, uint8_t* out, long long ldo, int rows,
                       int cols, float inv_scale, cudaStream_t stream) {
   if (rows == 0) return;

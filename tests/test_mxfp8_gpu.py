@@ -1,0 +1,75 @@
+"""MXFP8 (OCP microscaling: e4m3 values, e8m0 scale per 32 elements) on the block-scaled tensor
+cores (``tcgen05.mma kind::mxf8f6f4.block_scale``) against fp32 oracles: the device quantizer
+bit for bit against the host one, then every GEMM layout (decode swapped split-K fp32, prefill
+bf16, transposed bf16 store, row-major fp32 split-K) against the fp32 product of the dequantized
+MXFP8 operands."""
+import pytest
+import torch
+
+from vllm_neuron_b200.ops import linear as L
+
+pytestmark = pytest.mark.gpu
+
+
+def _rel(a, b):
+    a, b = a.float(), b.float()
+    return float((a - b).norm() / (b.norm() + 1e-12))
+
+
+def _x(M, K, dev, seed):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    # rows and 32-groups of very different magnitudes exercise the per-group exponents
+    x = torch.randn(M, K, generator=g) * torch.exp(torch.randn(M, K // 32, generator=g) * 2).repeat_interleave(32, 1)
+    return x.to(dev, torch.bfloat16)
+
+
+@pytest.mark.parametrize("M,K", [(1, 128), (7, 512), (130, 1024), (300, 4096)])
+def test_quant_mx8_matches_host(cuda_device, M, K):
+    from vllm_neuron_b200.ops._ext import ext
+
+    x = _x(M, K, cuda_device, M + K)
+    x[0, :32] = 0  # an all-zero group: scale 2^0
+    q = torch.empty(M, K, dtype=torch.float8_e4m3fn, device=cuda_device)
+    sf = torch.zeros(-(-M // 128), K // 128, 512, dtype=torch.uint8, device=cuda_device)
+    ext().quant_mx8(x, q, sf)
+    torch.cuda.synchronize()
+    qr, sr = L.quantize_mx8(x.cpu())
+    assert torch.equal(q.cpu().view(torch.uint8), qr.view(torch.uint8))
+    assert torch.equal(sf.cpu(), L.mx8_atoms(sr))
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 1024, 4096), (16, 768, 1024), (33, 4096, 1024), (64, 1280, 2048),
+                                   (100, 512, 512), (8, 200, 256)])
+def test_mx8_decode_accumulate(cuda_device, M, N, K):
+    w = L.MXFP8Weight.from_weight(_x(N, K, cuda_device, N).float() * 0.02)
+    x = _x(M, K, cuda_device, M)
+    ref = L._mx8_ref(x.cpu().float(), L.MXFP8Weight(w.q.cpu(), w.scales.cpu()))
+    for splits in (None, 1, 4):
+        acc = torch.zeros(M, N, dtype=torch.float32, device=cuda_device)
+        L.gemm_accumulate(x, w, acc, splits=splits)
+        torch.cuda.synchronize()
+        assert _rel(acc.cpu(), ref) < 1e-4, splits
+
+
+@pytest.mark.parametrize("M,N,K", [(300, 1024, 4096), (1024, 4096, 1024), (129, 384, 640), (8, 1536, 2048)])
+def test_mx8_bf16_out(cuda_device, M, N, K):
+    w = L.MXFP8Weight.from_weight(_x(N, K, cuda_device, N + 1).float() * 0.02)
+    x = _x(M, K, cuda_device, M + 1)
+    ref = L._mx8_ref(x.cpu().float(), L.MXFP8Weight(w.q.cpu(), w.scales.cpu()))
+    out = L.gemm_out(x, w)
+    torch.cuda.synchronize()
+    assert _rel(out.cpu(), ref) < 5e-3
+    # against the unquantized product: the MXFP8 rounding of both operands only
+    exact = x.cpu().float() @ (_x(N, K, cuda_device, N + 1).float().cpu() * 0.02).t()
+    assert _rel(out.cpu(), exact) < 0.15  # groups span e^(+-4) magnitudes: coarse e4m3 steps
+
+
+def test_mx8_row_major_splitk(cuda_device):
+    M, N, K = 512, 1024, 2048
+    w = L.MXFP8Weight.from_weight(_x(N, K, cuda_device, 5).float() * 0.02)
+    x = _x(M, K, cuda_device, 6)
+    ref = L._mx8_ref(x.cpu().float(), L.MXFP8Weight(w.q.cpu(), w.scales.cpu()))
+    acc = torch.zeros(M, N, dtype=torch.float32, device=cuda_device)
+    L.gemm_accumulate(x, w, acc, splits=2)
+    torch.cuda.synchronize()
+    assert _rel(acc.cpu(), ref) < 1e-4

@@ -114,10 +114,11 @@ def build_model(args: EngineArgs, tp: GroupComm = SINGLE):
             raise ValueError(f"vision tp_size {vcfg.tp_size} does not match the vision TP group "
                              f"({model.visual.tp.world} ranks)")
         model.configure_vision(vcfg, cuda_graphs=b200_config.cuda_graphs)
+    ck_info = {}
     if args.load_format == "dummy" or model_path is None:
         model.init_random(seed=args.seed)
     else:
-        load_checkpoint_into(model, model_path)
+        ck_info = load_checkpoint_into(model, model_path)
     fp8_scales = _static_fp8_scales(model_path) if model_path is not None else None
     if fp8_scales is not None or b200_config.quantization == "fp8_static":
         if not hasattr(model, "quantize_fp8_static"):
@@ -133,6 +134,14 @@ def build_model(args: EngineArgs, tp: GroupComm = SINGLE):
         if not hasattr(model, "quantize_block_fp8"):
             raise ValueError(f"{type(model).__name__} does not support block-FP8 linears")
         model.quantize_block_fp8()
+    if b200_config.quantization == "mxfp8" or (
+            ck_info.get("mxfp8") and device.type == "cuda" and dtype == torch.bfloat16
+            and b200_config.quantization not in ("bf16", "none")):
+        # MXFP8: random-init weights quantized with quantization="mxfp8", or an MXFP8
+        # checkpoint (read as its exact bf16 values) served on the block-scaled tensor cores
+        if not hasattr(model, "quantize_mxfp8"):
+            raise ValueError(f"{type(model).__name__} does not support MXFP8 linears")
+        model.quantize_mxfp8()
     if args.kv_cache_dtype not in (None, "auto"):
         if not hasattr(model, "set_kv_cache_dtype"):
             raise ValueError(f"{type(model).__name__} does not support kv_cache_dtype={args.kv_cache_dtype!r}")

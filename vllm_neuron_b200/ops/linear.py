@@ -119,6 +119,123 @@ class BlockFP8Weight:
         return self.dequant(torch.float32).to(torch.bfloat16)
 
 
+def mx8_exponents(amax: torch.Tensor) -> torch.Tensor:
+    """Unbiased e8m0 exponents of MXFP8 groups: the smallest ``e`` with ``amax <= 448 * 2^e``
+    (0 for all-zero groups), clamped to the e8m0 range [-127, 127].  Read from the fp32 bits so
+    that every device agrees exactly."""
+    bits = amax.float().contiguous().view(torch.int32)
+    e = ((bits >> 23) & 0xFF) - 135 + ((bits & 0x7FFFFF) > 0x600000).to(torch.int32)
+    e = torch.where(amax == 0, torch.zeros_like(e), e)
+    return e.clamp(-127, 127)
+
+
+def _pow2(e: torch.Tensor) -> torch.Tensor:
+    """Exact fp32 ``2^e`` for integer ``e`` in [-127, 127] (the e8m0 range)."""
+    bits = torch.where(e <= -127, torch.full_like(e, 0x00400000), (e + 127).clamp(1, 254) << 23)
+    return bits.to(torch.int32).view(torch.float32)
+
+
+def quantize_mx8(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """OCP MXFP8 of ``x [..., K]`` (K a multiple of 32): e4m3 values and biased e8m0 scales
+    ``[..., K / 32]`` (uint8), true value = ``q * 2^(s - 127)``.  Bit-identical to the device
+    quantizer (power-of-two scaling, then round-to-nearest-even e4m3)."""
+    *lead, K = x.shape
+    g = x.float().reshape(-1, K // 32, 32)
+    e = mx8_exponents(g.abs().amax(-1))
+    q = (g * _pow2(-e)[..., None]).to(torch.float8_e4m3fn)
+    return q.reshape(*lead, K), (e + 127).to(torch.uint8).reshape(*lead, K // 32)
+
+
+def mx8_atoms(scales: torch.Tensor, rows: int | None = None) -> torch.Tensor:
+    """Linear e8m0 scales ``[R, K / 32]`` -> the block-scaled GEMM's 512-byte atoms
+    ``[ceil(R / 128), K / 128, 512]``: atom (row block, 128-wide k block) holds row r's four
+    group scales at ``(r % 32) * 16 + ((r / 32) % 4) * 4``; rows past ``R`` are zero."""
+    R, G = scales.shape
+    assert G % 4 == 0, "K must be a multiple of 128"
+    nb = -(-(rows or R) // 128)
+    pad = torch.zeros(nb * 128, G, dtype=torch.uint8, device=scales.device)
+    pad[:R] = scales
+    # r = rb * 128 + r4 * 32 + r32, g = kb * 4 + j  ->  [rb, kb, r32, r4, j]
+    return pad.view(nb, 4, 32, G // 4, 4).permute(0, 3, 2, 1, 4).contiguous().view(nb, G // 4, 512)
+
+
+def dequantize_mx8(q: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+    """fp32 ``q * 2^(s - 127)`` of an MXFP8 tensor."""
+    *lead, K = q.shape
+    e = scales.to(torch.int32) - 127
+    return (q.float().reshape(-1, K // 32, 32) * _pow2(e.reshape(-1, K // 32))[..., None]).reshape(*lead, K)
+
+
+class MXFP8Weight:
+    """MXFP8 weight ``[N, K]`` (OCP microscaling: e4m3 values, one e8m0 scale per 32 elements
+    along K), the format of LLM-Compressor MXFP8 checkpoints (``weight`` F8_E4M3 +
+    ``weight_scale`` U8 ``[N, K / 32]``).  Served W8A8 on the block-scaled tensor cores
+    (``tcgen05.mma kind::mxf8f6f4.block_scale``): activations are quantized to MXFP8 per token and
+    32 elements, both operands stream as bytes and the hardware applies the scales.  K must be a
+    multiple of 128."""
+
+    def __init__(self, q: torch.Tensor, scales: torch.Tensor):
+        assert q.dtype == torch.float8_e4m3fn and q.dim() == 2 and scales.dtype == torch.uint8
+        assert q.shape[1] % 128 == 0 and tuple(scales.shape) == (q.shape[0], q.shape[1] // 32)
+        self.q = q.contiguous()
+        self.scales = scales.contiguous()
+        self.sf = mx8_atoms(self.scales)
+
+    @classmethod
+    def from_weight(cls, w: torch.Tensor) -> "MXFP8Weight":
+        q, s = quantize_mx8(w.detach())
+        return cls(q, s)
+
+    @property
+    def shape(self):
+        return self.q.shape
+
+    @property
+    def device(self):
+        return self.q.device
+
+    def dequant(self, dtype=torch.float32) -> torch.Tensor:
+        return dequantize_mx8(self.q, self.scales).to(dtype)
+
+    def dequant_bf16_ref(self) -> torch.Tensor:
+        """The weight as bf16 (exact: e4m3 times a power of two)."""
+        return self.dequant(torch.float32).to(torch.bfloat16)
+
+
+class MX8Activations:
+    """Reusable MXFP8 activation buffers of one projection input: e4m3 ``q [rows, K]`` and the
+    scale atoms (zeroed once, so padded rows of the last atom stay finite)."""
+
+    _cache: dict = {}
+    _retired: list = []  # outgrown buffers stay alive: CUDA graphs may have captured them
+
+    @classmethod
+    def get(cls, rows: int, K: int, device) -> tuple[torch.Tensor, torch.Tensor]:
+        key = (str(device), K)
+        cur = cls._cache.get(key)
+        if cur is None or cur[0].shape[0] < rows:
+            if cur is not None:
+                cls._retired.append(cur)
+            cap = max(rows, 128)
+            q = torch.empty(cap, K, dtype=torch.float8_e4m3fn, device=device)
+            sf = torch.zeros(-(-cap // 128), K // 128, 512, dtype=torch.uint8, device=device)
+            cur = cls._cache[key] = (q, sf)
+        return cur[0][:rows], cur[1]
+
+    @classmethod
+    def reserve(cls, rows: int, K: int, device):
+        """Allocate for ``rows`` up front (before graph capture)."""
+        cls.get(rows, K, device)
+
+
+def mx8_quantize_device(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """MXFP8 of bf16 activations on the GPU into reusable buffers: (q, scale atoms)."""
+    M, K = x.shape
+    q, sf = MX8Activations.get(M, K, x.device)
+    ext().quant_mx8(x, q, sf)
+    return q, sf
+
+
 # e2m1 code points (sign bit 3, exponent bits 2-1, mantissa bit 0)
 FP4_VALUES = [0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0, -0.0, -0.5, -1.0, -1.5, -2.0, -3.0, -4.0, -6.0]
 
@@ -311,6 +428,27 @@ def pick_splits(n_rows: int, k: int, sms: int, k_block: int = 64) -> int:
     return s
 
 
+def _mx8_ref(x: torch.Tensor, w: "MXFP8Weight") -> torch.Tensor:
+    """fp32 oracle of the MXFP8 GEMM: MXFP8-rounded activations times the MXFP8 weight."""
+    xq, xs = quantize_mx8(x)
+    return dequantize_mx8(xq, xs) @ w.dequant().t()
+
+
+def _mx8_bf16(x: torch.Tensor, w: "MXFP8Weight", out: torch.Tensor) -> torch.Tensor:
+    """bf16 ``out = x @ w^T`` on the block-scaled tensor cores: swapped operands and a
+    transposed store for decode batches (<= 64 tokens), tokens as the 128-row operand above."""
+    M = x.shape[0]
+    if not x.is_cuda:
+        out.copy_(_mx8_ref(x, w).to(out.dtype))
+        return out
+    xq, sf = mx8_quantize_device(x)
+    if M <= 64:
+        ext().gemm_mx8(w.q, xq, out, EPI_BF16_T, skinny_bn(M), 1, w.sf, sf)
+    else:
+        ext().gemm_mx8(xq, w.q, out, EPI_BF16, 128, 1, sf, w.sf)
+    return out
+
+
 def gemm_out(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,
              bn: int | None = None) -> torch.Tensor:
     """``out[M, N] = x[M, K] @ w[N, K]^T`` in bf16 (wide regime, no split-K)."""
@@ -318,6 +456,8 @@ def gemm_out(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,
     N = w.shape[0]
     if out is None:
         out = torch.empty((M, N), dtype=torch.bfloat16 if x.is_cuda else x.dtype, device=x.device)
+    if isinstance(w, MXFP8Weight):
+        return _mx8_bf16(x, w, out)
     if isinstance(w, FP8Weight):
         xq = quantize_fp8(x, w.in_scale)
         if not x.is_cuda:
@@ -353,7 +493,7 @@ def gemm_skinny_bf16(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None 
     """Decode regime without split-K: swapped operands, transposed bf16 store."""
     M, K = x.shape
     N = w.shape[0]
-    if isinstance(w, FP8Weight):  # row-major regime (no transposed FP8 store)
+    if isinstance(w, (FP8Weight, MXFP8Weight)):  # row-major regime (no transposed FP8 store)
         return gemm_out(x, w, out)
     if isinstance(w, BlockFP8Weight):
         if out is None:
@@ -383,6 +523,21 @@ def gemm_accumulate(x: torch.Tensor, w: torch.Tensor, acc: torch.Tensor,
     M, K = x.shape
     N = w.shape[0]
     assert acc.dtype == torch.float32 and acc.shape[0] >= M and acc.shape[1] == N
+    if isinstance(w, MXFP8Weight):
+        if not x.is_cuda:
+            acc[:M].add_(_mx8_ref(x, w))
+            return acc
+        xq, sf = mx8_quantize_device(x)
+        sms = num_sms(x.device)
+        if M <= SKINNY_MAX:
+            tiles = math.ceil(N / 128)
+            s = splits if splits is not None else (pick_splits(N, K, sms, 128) if tiles < sms else -1)
+            ext().gemm_mx8(w.q, xq, acc, EPI_F32_RED_T, skinny_bn(M), s, w.sf, sf)
+        else:
+            rows = math.ceil(M / 128) * 128 * math.ceil(N / 128)
+            s = splits if splits is not None else pick_splits(rows, K, sms, 128)
+            ext().gemm_mx8(xq, w.q, acc, EPI_F32_RED, 128, s, sf, w.sf)
+        return acc
     if isinstance(w, FP8Weight):
         xq = quantize_fp8(x, w.in_scale)
         if not x.is_cuda:
@@ -449,6 +604,14 @@ def gemm_silu(x: torch.Tensor, w_gu: torch.Tensor, out: torch.Tensor | None = No
     N2 = w_gu.shape[0]
     if out is None:
         out = torch.empty((M, N2 // 2), dtype=torch.bfloat16, device=x.device)
+    if isinstance(w_gu, MXFP8Weight):
+        if not x.is_cuda:
+            out.copy_(silu_mul_ref(_mx8_ref(x, w_gu), SILU_BLOCK).to(out.dtype))
+            return out
+        from .activation import silu_mul
+
+        gu = _mx8_bf16(x, w_gu, torch.empty((M, N2), dtype=torch.bfloat16, device=x.device))
+        return silu_mul(gu, out=out, blk=SILU_BLOCK)
     if isinstance(w_gu, FP8Weight):
         xq = quantize_fp8(x, w_gu.in_scale)
         if not x.is_cuda:

@@ -117,11 +117,18 @@ def fp8_aware_getter(get, names: set[str], block: tuple[int, int] | None):
             if si in names:
                 return dequant_block_fp8(t, get(si), blk, torch.float32)
             sc = name.replace(".weight", ".weight_scale")
-            if sc in names:  # per-tensor static scale
-                return t.float() * get(sc).float()
+            if sc in names:
+                s = get(sc)
+                if s.dtype == torch.uint8 and s.dim() == t.dim() and s.shape[-1] * 32 == t.shape[-1]:
+                    # MXFP8 (LLM-Compressor): one e8m0 scale per 32 elements, exact in bf16
+                    g.mxfp8 = True
+                    e = s.to(torch.int32) - 127
+                    return (t.float().unflatten(-1, (-1, 32)) * torch.exp2(e.float())[..., None]).flatten(-2)
+                return t.float() * s.float()  # per-tensor static scale
             return t.float()
         return t
 
+    g.mxfp8 = False  # set once an MXFP8 weight was read
     return g
 
 
@@ -130,8 +137,9 @@ def load_checkpoint_into(model, path: str) -> dict:
     ck = SafetensorsCheckpoint(path)
     warm = ck.warm_page_cache(model.tp.rank, model.tp.world)
     names = ck.names()
-    model.load_hf_state_dict(fp8_aware_getter(ck.get, names, getattr(model.cfg, "weight_block_size", None)), names)
+    getter = fp8_aware_getter(ck.get, names, getattr(model.cfg, "weight_block_size", None))
+    model.load_hf_state_dict(getter, names)
     warm.join(timeout=0)
     if torch.cuda.is_available() and model.device.type == "cuda":
         torch.cuda.synchronize(model.device)
-    return {"seconds": time.perf_counter() - t0, "bytes": ck.bytes_read}
+    return {"seconds": time.perf_counter() - t0, "bytes": ck.bytes_read, "mxfp8": getter.mxfp8}
