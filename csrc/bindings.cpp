@@ -281,6 +281,86 @@ void quant_mx8(const at::Tensor& x, at::Tensor& q, at::Tensor& sf) {
   check_launch("quant_mx8");
 }
 
+// MXFP8 of expert-sorted rows x [R, kvalid] (bf16) into q [R, K] (K >= kvalid, a multiple of 128;
+// columns past kvalid are zeros) and per-entry scale atoms sf [gmax, K / 128, 512].
+void quant_mx8_tiles(const at::Tensor& x, at::Tensor& q, at::Tensor& sf, const at::Tensor& gtiles,
+                     const at::Tensor& gcount) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  TORCH_CHECK(q.scalar_type() == at::kFloat8_e4m3fn && sf.scalar_type() == at::kByte, "quant_mx8_tiles: q e4m3, sf uint8");
+  TORCH_CHECK(x.dim() == 2 && q.dim() == 2 && x.stride(1) == 1 && q.stride(1) == 1 && sf.is_contiguous() &&
+                  gtiles.is_contiguous() && gtiles.size(-1) == 4, "quant_mx8_tiles: layouts");
+  const int64_t K = q.size(1), gmax = gtiles.size(0);
+  TORCH_CHECK(q.size(0) >= x.size(0) && x.size(1) <= K && sf.numel() >= gmax * (K / 128) * 512,
+              "quant_mx8_tiles: output shapes");
+  const c10::cuda::CUDAGuard guard(x.device());
+  b200::quant_mx8_tiles_launch(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0),
+                               reinterpret_cast<uint8_t*>(q.data_ptr()), q.stride(0), sf.data_ptr<uint8_t>(),
+                               gtiles.data_ptr<int>(), gcount.data_ptr<int>(), (int)gmax, (int)K, (int)x.size(1),
+                               cur_stream());
+  check_launch("quant_mx8_tiles");
+}
+
+// Grouped MXFP8 expert GEMM.  grouped_t = 0 (prefill): a = expert-sorted token rows [R, K] with
+// per-entry atoms sfa, b = stacked expert weights [E, N, K] (N a multiple of 128) with atoms sfb
+// over the stacked rows, EPI_BF16 out[R, N], bn 128.  grouped_t = 1 (decode): a = stacked weights
+// [E, M, K] (M a multiple of 128), b = token rows [R, K] with per-entry atoms, EPI_BF16_T
+// out[R, M] with bn >= the tokens of any expert.
+void gemm_mx8_grouped(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, int64_t epi, int64_t bn,
+                      const at::Tensor& sfa, const at::Tensor& sfb, const at::Tensor& gtiles,
+                      const at::Tensor& gcount, int64_t grouped_t) {
+  CHECK_CUDA(a);
+  CHECK_CUDA(b);
+  CHECK_BF16(out);
+  TORCH_CHECK(a.scalar_type() == at::kFloat8_e4m3fn && b.scalar_type() == at::kFloat8_e4m3fn,
+              "gemm_mx8_grouped: operands must be float8_e4m3fn");
+  TORCH_CHECK(a.is_contiguous() && b.is_contiguous() && out.stride(1) == 1 && sfa.is_contiguous() &&
+                  sfb.is_contiguous() && sfa.scalar_type() == at::kByte && sfb.scalar_type() == at::kByte,
+              "gemm_mx8_grouped: layouts");
+  const c10::cuda::CUDAGuard guard(a.device());
+  b200::GemmArgs g{};
+  g.A = a.data_ptr();
+  g.B = b.data_ptr();
+  g.out = out.data_ptr();
+  g.lda = a.size(-1);
+  g.ldb = b.size(-1);
+  g.ldo = out.stride(0);
+  g.K = (int)a.size(-1);
+  TORCH_CHECK(b.size(-1) == g.K && g.K % 128 == 0, "gemm_mx8_grouped: K");
+  if (grouped_t) {
+    TORCH_CHECK(a.dim() == 3 && b.dim() == 2 && epi == b200::EPI_BF16_T, "gemm_mx8_grouped: a [E, M, K], b [R, K]");
+    TORCH_CHECK(out.size(0) >= b.size(0) && out.size(1) >= a.size(1), "gemm_mx8_grouped: out");
+    g.M = (int)a.size(1);
+    g.N = (int)b.size(0);
+    g.num_groups = (int)a.size(0);
+    g.grouped_t = 1;
+    TORCH_CHECK(sfa.numel() >= a.size(0) * a.size(1) / 128 * (g.K / 128) * 512 &&
+                    sfb.numel() >= gtiles.size(0) * (g.K / 128) * 512, "gemm_mx8_grouped: scale atoms");
+  } else {
+    TORCH_CHECK(a.dim() == 2 && b.dim() == 3 && epi == b200::EPI_BF16, "gemm_mx8_grouped: a [R, K], b [E, N, K]");
+    TORCH_CHECK(out.size(0) >= a.size(0) && out.size(1) >= b.size(1), "gemm_mx8_grouped: out");
+    g.M = (int)a.size(0);
+    g.N = (int)b.size(1);
+    g.num_groups = (int)b.size(0);
+    TORCH_CHECK(sfb.numel() >= b.size(0) * b.size(1) / 128 * (g.K / 128) * 512 &&
+                    sfa.numel() >= gtiles.size(0) * (g.K / 128) * 512, "gemm_mx8_grouped: scale atoms");
+  }
+  g.gtiles = gtiles.data_ptr<int>();
+  g.gcount = gcount.data_ptr<int>();
+  g.gmax = (int)gtiles.size(0);
+  g.bn = (int)bn;
+  g.epi = (int)epi;
+  g.splits = 1;
+  g.status = status_word();
+  g.fp8 = 1;
+  g.w8 = 6;
+  g.sfa = sfa.data_ptr<uint8_t>();
+  g.sfb = sfb.data_ptr<uint8_t>();
+  if (g.M == 0 || g.N == 0) return;
+  b200::gemm_bf16_launch(g, cur_stream());
+  check_launch("gemm_mx8_grouped");
+}
+
 // MXFP8 x MXFP8 GEMM on the block-scaled tensor cores: out = a @ b^T with a [M, K], b [N, K] e4m3
 // and their scale atoms (see quant_mx8).  epi: EPI_BF16 (bn 128, bf16 out[M, N]), EPI_BF16_T
 // (bf16 out[N, M]), EPI_F32_RED_T (fp32 out[N, M] +=, split-K) or EPI_F32_RED (fp32 out[M, N] +=).
@@ -1262,6 +1342,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("quant_fp8_block", &quant_fp8_block);
   m.def("quant_mx8", &quant_mx8);
   m.def("gemm_mx8", &gemm_mx8);
+  m.def("quant_mx8_tiles", &quant_mx8_tiles);
+  m.def("gemm_mx8_grouped", &gemm_mx8_grouped);
   m.def("quant_fp8", &quant_fp8);
   m.def("rmsnorm_quant", &rmsnorm_quant);
   m.def("sp_norm_push", &sp_norm_push);

@@ -13,6 +13,7 @@
 #include <stdint.h>
 
 #include <atomic>
+#include <cstdlib>
 #include <utility>
 
 #ifndef B200_WAIT_TIMEOUT_NS
@@ -417,6 +418,15 @@ __device__ __forceinline__ T warp_max(T v) {
 }
 
 #ifndef __CUDACC_RTC__
+// VLLM_B200_DISABLE_PDL=1 launches every kernel in plain stream order (a debugging switch).
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("VLLM_B200_DISABLE_PDL");
+    return !(e != nullptr && e[0] == '1');
+  }();
+  return on;
+}
+
 // Launch with programmatic stream serialization (see pdl_wait / pdl_trigger).
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
@@ -430,7 +440,7 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 

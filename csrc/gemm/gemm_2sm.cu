@@ -217,7 +217,6 @@ __global__ void __launch_bounds__(192, 1)
         }
       }
       if (!waited) pdl_wait();
-      pdl_trigger();
       if (!ok && rank == 0) {
         const uint32_t first = it > (uint32_t)kStages2 ? it - kStages2 : 0;
         for (uint32_t j = first; j < it; ++j)
@@ -373,15 +372,18 @@ void launch2(const CUtensorMap& ta, const CUtensorMap& tb, const Gemm2Params& p,
   cfg.blockDim = dim3(192);
   cfg.dynamicSmemBytes = kSmem2;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[2];
+  // Plain stream order (no programmatic dependent launch): with the pair kernel launched early,
+  // the hybrid model's prefill (DeltaNet / MoE kernels between its CTA-pair GEMMs) stopped
+  // making progress on the GPU in 4 of 4 serving runs, and ran to completion with either the
+  // pair kernel or programmatic launch switched off.  The kernel does not trigger its
+  // successors either, so it never overlaps a neighbouring kernel.
+  cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 2;
+  cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, p);
   if (e != cudaSuccess) throw std::runtime_error(std::string("gemm2sm launch: ") + cudaGetErrorString(e));
 }

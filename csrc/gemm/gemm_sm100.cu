@@ -369,17 +369,21 @@ __global__ void __launch_bounds__((W8 >= 1 && W8 <= 4) ? 320 : 192, 1)
         }
         uint8_t* dst = kWSide == 1 ? smS + s * kSBytes : smA + s * kATileBytes;
         tma_load_2d(&tmA, &full_bar[s], dst, (kFP4 && kWSide == 1) ? kb * kSRow : kb * kKElems, a_row, hint_a);
-        if constexpr (kMX)
-          bulk_load_1d(smSF + s * kSFBytes, p.sfa + ((long long)(a_row >> 7) * p.sf_kb + kb) * 512, 512,
-                       &full_bar[s], hint_a);
+        if constexpr (kMX) {
+          // grouped prefill: A = expert-sorted tokens, one scale atom per tile-list entry
+          const long long atom = p.grouped == 1 ? (long long)mb : (long long)(a_row >> 7);
+          bulk_load_1d(smSF + s * kSFBytes, p.sfa + (atom * p.sf_kb + kb) * 512, 512, &full_bar[s], hint_a);
+        }
       };
       auto load_b = [&](int s, int kb, int nb, int mb) {
         const int row = p.grouped == 2 ? p.gtiles[mb].y : (p.grouped ? tile_rows(p, mb).b_base : 0) + nb * BN;
         uint8_t* dst = kWSide == 2 ? smS + s * kSBytes : smB + s * kBTileBytes;
         tma_load_2d(&tmB, &full_bar[s], dst, (kFP4 && kWSide == 2) ? kb * kSRow : kb * kKElems, row, hint_b);
-        if constexpr (kMX)
-          bulk_load_1d(smSF + s * kSFBytes + 512, p.sfb + ((long long)(row >> 7) * p.sf_kb + kb) * 512, 512,
-                       &full_bar[s], hint_b);
+        if constexpr (kMX) {
+          // swapped grouped decode: B = the entry's tokens, one scale atom per entry
+          const long long atom = p.grouped == 2 ? (long long)mb : (long long)(row >> 7);
+          bulk_load_1d(smSF + s * kSFBytes + 512, p.sfb + (atom * p.sf_kb + kb) * 512, 512, &full_bar[s], hint_b);
+        }
       };
       // The grouped tile list is written by the previous kernel.
       if (p.grouped) pdl_wait();
@@ -492,7 +496,8 @@ __global__ void __launch_bounds__((W8 >= 1 && W8 <= 4) ? 320 : 192, 1)
             tmem_cp_32x128b_warpx4(sf_a, make_sdesc_none(sf_src, 128, 128));
             tmem_cp_32x128b_warpx4(sf_b, make_sdesc_none(sf_src + 512, 128, 128));
             // B rows of this tile start (nb * BN) % 128 rows into their atom: 32 rows per column
-            const uint32_t b_col = (uint32_t)(((nb * BN) & 127) >> 5);
+            // (in the swapped grouped mode nb indexes the weight's 128-row blocks; B starts its atom)
+            const uint32_t b_col = p.grouped == 2 ? 0u : (uint32_t)(((nb * BN) & 127) >> 5);
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
               const uint64_t adesc = make_sdesc_sw128(a_addr + k * 32);
@@ -978,8 +983,10 @@ void gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
     throw std::invalid_argument("gemm: grouped mode needs splits == 1, groups and a tile bound");
   if (a.grouped_t && (!grouped || a.epi != EPI_BF16_T || a.w8 == 2 || a.w8 == 4))
     throw std::invalid_argument("gemm: swapped grouped mode needs a tile list, EPI_BF16_T and the weight as A");
-  if (a.fp8 && (grouped || a.sp != nullptr))
-    throw std::invalid_argument("gemm: FP8 operands are for the dense (non-grouped, non-SP) modes");
+  if (a.fp8 && a.sp != nullptr)
+    throw std::invalid_argument("gemm: FP8 operands are for the non-SP modes");
+  if (a.fp8 && grouped && a.w8 != 6)
+    throw std::invalid_argument("gemm: grouped FP8 operands need MXFP8 scales (w8 = 6)");
   const uint64_t b_rows = grouped && !a.grouped_t ? (uint64_t)a.N * a.num_groups : (uint64_t)a.N;
   // A rows: the stacked experts' weights in the swapped grouped mode
   const uint64_t a_rows = a.grouped_t ? (uint64_t)a.M * a.num_groups : (uint64_t)a.M;
@@ -1015,12 +1022,16 @@ void gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
   } else if (a.w8 == 6) {
     const bool ok_epi = (a.epi == EPI_BF16 && a.bn == 128) || a.epi == EPI_BF16_T || a.epi == EPI_F32_RED_T ||
                         (a.epi == EPI_F32_RED && a.bn == 128);
-    if (!a.fp8 || a.sfa == nullptr || a.sfb == nullptr || grouped || a.sp != nullptr || a.K % 128 != 0 ||
-        !ok_epi || (a.bn != 16 && a.bn != 32 && a.bn != 64 && a.bn != 128) || (a.bn == 16 && a.N > 16) ||
-        (a.epi == EPI_BF16_T && a.bn == 128))
+    // grouped: the token operand's scales are per tile-list entry (atom = entry), the stacked
+    // weight's per 128 rows, so an expert's weight rows must fill whole atoms
+    const bool bad_grouped = grouped && (a.grouped_t ? (a.M % 128 != 0 || a.epi != EPI_BF16_T)
+                                                     : (a.N % 128 != 0 || a.epi != EPI_BF16));
+    if (!a.fp8 || a.sfa == nullptr || a.sfb == nullptr || a.sp != nullptr || a.K % 128 != 0 || bad_grouped ||
+        !ok_epi || (a.bn != 16 && a.bn != 32 && a.bn != 64 && a.bn != 128) ||
+        (a.bn == 16 && a.N > 16 && !a.grouped_t) || (a.epi == EPI_BF16_T && a.bn == 128))
       throw std::invalid_argument("gemm: MXFP8 needs e4m3 operands with both scale atoms, K in 128s, N tile "
                                   "16 (N <= 16) / 32 / 64 / 128 and EPI_BF16 (bn 128), EPI_BF16_T, "
-                                  "EPI_F32_RED_T or EPI_F32_RED");
+                                  "EPI_F32_RED_T or EPI_F32_RED; grouped: 128-row experts");
   } else if (a.w8 != 0) {
     throw std::invalid_argument("gemm: w8 must be 0..6");
   }

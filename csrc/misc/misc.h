@@ -54,6 +54,9 @@ void quant_fp8_launch(const __nv_bfloat16* x, long long ldx, uint8_t* out, long 
 // Per-token, per-128-column dynamic quantization (scales [rows][lds], max|x| / 448).
 void quant_mx8_launch(const __nv_bfloat16* x, long long ldx, uint8_t* out, long long ldo, uint8_t* sf,
                       int rows, int cols, cudaStream_t stream);
+void quant_mx8_tiles_launch(const __nv_bfloat16* x, long long ldx, uint8_t* out, long long ldo, uint8_t* sf,
+                            const int* tiles, const int* count, int gmax, int cols, int kvalid,
+                            cudaStream_t stream);
 void quant_fp8_block_launch(const __nv_bfloat16* x, long long ldx, uint8_t* out, long long ldo,
                             float* scales, int lds, int rows, int cols, cudaStream_t stream);
 // row_scales == null: static per-tensor scale; else per-row dynamic scales (max|y| / 448).

@@ -189,6 +189,58 @@ __global__ void __launch_bounds__(256) quant_mx8_kernel(const __nv_bfloat16* __r
   }
 }
 
+// The same for the expert-sorted rows of a grouped GEMM: the scales go into one atom per
+// tile-list entry (entry t covers rows [first, min(first + 128, end)) of its expert; row
+// first + i is atom row i), the layout the grouped block-scaled GEMM reads for its token operand.
+// Columns at or past `kvalid` are quantized as zeros (K padded to a multiple of 128).
+// grid (gmax, ceil(nblk / 8)), 8 warps, one 128-column block per warp.
+__global__ void __launch_bounds__(256) quant_mx8_tiles_kernel(const __nv_bfloat16* __restrict__ x, long long ldx,
+                                                              uint8_t* __restrict__ out, long long ldo,
+                                                              uint8_t* __restrict__ sf, const int4* __restrict__ tiles,
+                                                              const int* __restrict__ count, int nblk, int kvalid) {
+  pdl_trigger();
+  pdl_wait();
+  const int t = blockIdx.x;
+  const int b = blockIdx.y * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= *count || b >= nblk) return;
+  const int4 g = tiles[t];
+  const int r1 = min(g.y + 128, g.z);
+  const int c = b * 128 + lane * 4;
+  for (int r = g.y; r < r1; ++r) {
+    float2 a = make_float2(0.f, 0.f), d = make_float2(0.f, 0.f);
+    if (c < kvalid) {  // kvalid % 4 == 0: a lane's 4 columns are all valid or all padding
+      const uint2 v = *reinterpret_cast<const uint2*>(x + (long long)r * ldx + c);
+      a = unpack_bf16x2(v.x);
+      d = unpack_bf16x2(v.y);
+    }
+    float m = fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(d.x), fabsf(d.y)));
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const uint32_t bits = __float_as_uint(m);
+    int e = (int)((bits >> 23) & 0xffu) - 135 + ((bits & 0x7fffffu) > 0x600000u ? 1 : 0);
+    if (m == 0.f) e = 0;
+    e = max(-127, min(127, e));
+    const float inv = e >= 127 ? __uint_as_float(0x00400000u) : __uint_as_float((uint32_t)(127 - e) << 23);
+    *reinterpret_cast<uint32_t*>(out + (long long)r * ldo + c) = q4(a.x * inv, a.y * inv, d.x * inv, d.y * inv);
+    if ((lane & 7) == 0) {
+      const int ri = r - g.y;
+      sf[((long long)t * nblk + b) * 512 + (ri & 31) * 16 + (ri >> 5) * 4 + (lane >> 3)] = (uint8_t)(e + 127);
+    }
+  }
+}
+
+void quant_mx8_tiles_launch(const __nv_bfloat16* x, long long ldx, uint8_t* out, long long ldo, uint8_t* sf,
+                            const int* tiles, const int* count, int gmax, int cols, int kvalid,
+                            cudaStream_t stream) {
+  if (gmax == 0) return;
+  if (cols % 128 != 0 || kvalid % 4 != 0 || kvalid > cols || ldx % 4 != 0 || ldo % 4 != 0)
+    throw std::invalid_argument("quant_mx8_tiles: columns must be a multiple of 128, valid columns of 4");
+  const int nblk = cols / 128;
+  launch_pdl(quant_mx8_tiles_kernel, dim3(gmax, (nblk + 7) / 8), dim3(256), 0, stream, x, ldx, out, ldo, sf,
+             reinterpret_cast<const int4*>(tiles), count, nblk, kvalid);
+}
+
 void quant_mx8_launch(const __nv_bfloat16* x, long long ldx, uint8_t* out, long long ldo, uint8_t* sf,
                       int rows, int cols, cudaStream_t stream) {
   if (rows == 0) return;

@@ -73,3 +73,26 @@ def test_mx8_row_major_splitk(cuda_device):
     L.gemm_accumulate(x, w, acc, splits=2)
     torch.cuda.synchronize()
     assert _rel(acc.cpu(), ref) < 1e-4
+
+
+@pytest.mark.parametrize("T", [1, 7, 40, 300])
+def test_mx8_grouped_experts(cuda_device, T):
+    """MXFP8 expert stacks through the grouped block-scaled GEMM (swapped decode layout up to 64
+    tokens, expert-sorted token tiles above) against the fp32 per-token oracle fed with the
+    MXFP8-rounded input rows; the hidden activation's MXFP8 rounding is inside the tolerance."""
+    from vllm_neuron_b200.ops import moe as MO
+
+    E, H, I, k = 8, 512, 256, 2
+    g = torch.Generator(device="cpu").manual_seed(T)
+    wgu = L.MXFP8Weight.from_weight((torch.randn(E, 2 * I, H, generator=g) * 0.05).to(cuda_device))
+    wd = L.MXFP8Weight.from_weight((torch.randn(E, H, I, generator=g) * 0.05).to(cuda_device))
+    x = (torch.randn(T, H, generator=g)).to(cuda_device, torch.bfloat16)
+    ids = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)]).to(cuda_device, torch.int32)
+    w = torch.rand(T, k, generator=g).to(cuda_device)
+    out = MO.moe_experts(x, ids, w, wgu, wd)
+    torch.cuda.synchronize()
+    xq, xs = L.quantize_mx8(x.float())
+    ref = MO.experts_ref(L.dequantize_mx8(xq, xs), ids, w, wgu, wd)
+    assert _rel(out, ref) < 4e-2
+    # against the unquantized activations too (both roundings)
+    assert _rel(out, MO.experts_ref(x.float(), ids, w, wgu, wd)) < 8e-2

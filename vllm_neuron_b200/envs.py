@@ -65,6 +65,9 @@ _flag("KV_CACHE_MAX_GIB", _float, None, "cap of the KV-cache budget per GPU (GiB
 _flag("MIN_KV_BUDGET_GIB", _float, 0.0, "refuse to start when the KV budget is below this (GiB)")
 _flag("SKIP_WARMUP", _bool, False, "skip the warm-up passes at start-up")
 _flag("DISABLE_CUDA_GRAPHS", _bool, False, "run decode eagerly (no CUDA-graph capture)")
+_flag("DISABLE_PDL", _bool, False,
+      "launch kernels in plain stream order instead of programmatic dependent launch "
+      "(read by the native library at its first launch)")
 _flag("DISABLE_TC_ATTENTION", _bool, False,
       "run prefill attention on the mma.sync kernel instead of the tcgen05 kernel")
 _flag("DISABLE_FUSED_COMM", _bool, False,

@@ -310,17 +310,20 @@ class LlamaForCausalLM(torch.nn.Module):
     def quantize_mxfp8(self) -> int:
         """Switch the dense 2-D projections (K a multiple of 128) to MXFP8 weights: e4m3 values
         with one e8m0 scale per 32 input elements, served W8A8 on the block-scaled tensor cores
-        (activations quantized to MXFP8 per token on the fly).  An MXFP8 checkpoint, loaded as
-        its exact bf16 dequantization, re-quantizes to the same values (power-of-two scales).
-        Expert stacks stay in their format.  Reference: the MXFP8 text decoder of Qwen3-VL
+        (activations quantized to MXFP8 per token on the fly); bf16 expert stacks with 128-row
+        experts and K in 128s run on the grouped form of the same GEMM.  An MXFP8 checkpoint,
+        loaded as its exact bf16 dequantization, re-quantizes to the same values (power-of-two
+        scales).  MXFP4 expert stacks stay in their format.  Reference: the MXFP8 text decoder of Qwen3-VL
         (vllm_neuron/model/qwen3_vl/model_mxfp8.py) and the MX linears of
         vllm_neuron/model/llama3/model_mx_fp8.py."""
         n = 0
         for ly in self.layers:
             for name in self.BLOCK_FP8_PARAMS:
                 w = getattr(ly, name, None)
-                if w is None or not isinstance(w, torch.Tensor) or w.dim() != 2 or w.shape[1] % 128:
+                if w is None or not isinstance(w, torch.Tensor) or w.dim() not in (2, 3) or w.shape[-1] % 128:
                     continue
+                if w.dim() == 3 and w.shape[1] % 128:
+                    continue  # the grouped MXFP8 GEMM needs 128-row experts
                 mw = L.MXFP8Weight.from_weight(w)
                 if name in getattr(ly, "_parameters", {}):
                     del ly._parameters[name]
@@ -330,7 +333,8 @@ class LlamaForCausalLM(torch.nn.Module):
         if self.device.type == "cuda":
             torch.cuda.empty_cache()
             # activation buffers at their largest size before any decode graph is captured
-            ks = {w.shape[1] for ly in self.layers for w in vars(ly).values() if isinstance(w, L.MXFP8Weight)}
+            ks = {w.shape[-1] for ly in self.layers for w in vars(ly).values()
+                  if isinstance(w, L.MXFP8Weight) and w.q.dim() == 2}
             for k in ks:
                 L.MX8Activations.reserve(self.max_tokens, k, self.device)
         return n

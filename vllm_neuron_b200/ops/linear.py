@@ -175,11 +175,14 @@ class MXFP8Weight:
     multiple of 128."""
 
     def __init__(self, q: torch.Tensor, scales: torch.Tensor):
-        assert q.dtype == torch.float8_e4m3fn and q.dim() == 2 and scales.dtype == torch.uint8
-        assert q.shape[1] % 128 == 0 and tuple(scales.shape) == (q.shape[0], q.shape[1] // 32)
+        assert q.dtype == torch.float8_e4m3fn and q.dim() in (2, 3) and scales.dtype == torch.uint8
+        K = q.shape[-1]
+        assert K % 128 == 0 and tuple(scales.shape) == (*q.shape[:-1], K // 32)
         self.q = q.contiguous()
         self.scales = scales.contiguous()
-        self.sf = mx8_atoms(self.scales)
+        # expert stacks [E, N, K]: atoms over the stacked rows (N a multiple of 128 for the
+        # grouped GEMM, so every expert starts an atom)
+        self.sf = mx8_atoms(self.scales.reshape(-1, K // 32))
 
     @classmethod
     def from_weight(cls, w: torch.Tensor) -> "MXFP8Weight":
@@ -196,6 +199,10 @@ class MXFP8Weight:
 
     def dequant(self, dtype=torch.float32) -> torch.Tensor:
         return dequantize_mx8(self.q, self.scales).to(dtype)
+
+    def __getitem__(self, e: int) -> "MXFP8Weight":
+        """Expert ``e`` of a stack."""
+        return MXFP8Weight(self.q[e], self.scales[e])
 
     def dequant_bf16_ref(self) -> torch.Tensor:
         """The weight as bf16 (exact: e4m3 times a power of two)."""

@@ -120,7 +120,7 @@ def route_ref(logits: torch.Tensor, k: int, mode: int, renorm: bool = True,
 
 def _dense(w):
     """bf16 tensor view of a weight (block-FP8 / MXFP4 weights: the bf16 operand the kernels use)."""
-    return w.dequant_bf16_ref() if isinstance(w, (L.BlockFP8Weight, L.MXFP4Weight)) else w
+    return w.dequant_bf16_ref() if isinstance(w, (L.BlockFP8Weight, L.MXFP4Weight, L.MXFP8Weight)) else w
 
 
 def experts_ref(x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, w_gu: torch.Tensor,
@@ -308,6 +308,32 @@ def moe_experts(x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, w_gu: torch
                          b_gu, b_down, act, alpha, limit, e_start, ws, out, None, None, None, None, 0)
 
 
+class _MX8TileBufs:
+    """MXFP8 buffers of the expert-sorted rows (values and per-entry scale atoms), per (device,
+    K); outgrown ones stay referenced because CUDA graphs may have captured them."""
+
+    cache: dict = {}
+    retired: list = []
+
+    @classmethod
+    def get(cls, rows: int, K: int, entries: int, device):
+        key = (str(device), K)
+        cur = cls.cache.get(key)
+        if cur is None or cur[0].shape[0] < rows or cur[1].shape[0] < entries:
+            if cur is not None:
+                cls.retired.append(cur)
+            r = max(rows, 128 if cur is None else cur[0].shape[0])
+            n = max(entries, 1 if cur is None else cur[1].shape[0])
+            cur = cls.cache[key] = (torch.empty(r, K, dtype=torch.float8_e4m3fn, device=device),
+                                    torch.zeros(n, K // 128, 512, dtype=torch.uint8, device=device))
+        return cur[0][:rows], cur[1]
+
+
+def _mx8_experts_ok(w_gu, w_down) -> bool:
+    return (isinstance(w_gu, L.MXFP8Weight) and isinstance(w_down, L.MXFP8Weight)
+            and w_gu.q.shape[1] % 128 == 0 and w_down.q.shape[1] % 128 == 0)
+
+
 def _experts_cuda(x, ids, w, w_gu, w_down, k, b_gu, b_down, act, alpha, limit, e_start, ws, out,
                   shared, shared_gate, fp4_gu, fp4_down, fp4_max_tokens):
     T, H = x.shape
@@ -318,6 +344,32 @@ def _experts_cuda(x, ids, w, w_gu, w_down, k, b_gu, b_down, act, alpha, limit, e
                     ws.inv_pos[:R], ws.gtiles, ws.gcount)
     xp = ws.xp[:R]
     ext().moe_gather(x, ws.sorted_src, k, ws.offsets, xp)
+    if _mx8_experts_ok(w_gu, w_down):
+        # MXFP8 experts on the block-scaled tensor cores: the sorted rows are quantized to MXFP8
+        # with one scale atom per tile-list entry; decode-size batches swap operands (expert
+        # weight rows as the 128-row operand, each expert's <= 64 tokens as the N tile)
+        gmax = ws.gtiles.shape[0]
+        swap = T <= SWAP_MAX_TOKENS
+        bn_t = L.skinny_bn(T) if swap else 0
+        gt = ws.gtiles[:min(gmax, R)] if swap else ws.gtiles
+        xq, sfx = _MX8TileBufs.get(R, H, gmax, x.device)
+        ext().quant_mx8_tiles(xp, xq, sfx, ws.gtiles, ws.gcount)
+        gu = ws.gu[:R]
+        if swap:
+            ext().gemm_mx8_grouped(w_gu.q, xq, gu, EPI_BF16_T, bn_t, w_gu.sf, sfx, gt, ws.gcount, 1)
+        else:
+            ext().gemm_mx8_grouped(xq, w_gu.q, gu, EPI_BF16, 128, sfx, w_gu.sf, gt, ws.gcount, 0)
+        a = ws.act[:R, :I]
+        ext().moe_act(gu, b_gu, ws.row_expert, ws.offsets, act, alpha, limit, a)
+        aq, sfa = _MX8TileBufs.get(R, I, gmax, x.device)
+        ext().quant_mx8_tiles(a, aq, sfa, ws.gtiles, ws.gcount)
+        y = ws.y[:R]
+        if swap:
+            ext().gemm_mx8_grouped(w_down.q, aq, y, EPI_BF16_T, bn_t, w_down.sf, sfa, gt, ws.gcount, 1)
+        else:
+            ext().gemm_mx8_grouped(aq, w_down.q, y, EPI_BF16, 128, sfa, w_down.sf, gt, ws.gcount, 0)
+        ext().moe_combine(y, ws.inv_pos[:R], w, ids, b_down, e_start, shared, shared_gate, out)
+        return out
     gu = ws.gu[:R]
     use_fp4 = fp4_gu is not None and T <= fp4_max_tokens
     # decode-size MXFP4 batches: swapped grouped tcgen05 GEMM (expert weight rows as the 128-row
