@@ -1153,7 +1153,7 @@ void moe_combine(const at::Tensor& y, const at::Tensor& inv_pos, const at::Tenso
   CHECK_CUDA(y);
   CHECK_BF16(y);
   CHECK_BF16(out);
-  TORCH_CHECK(y.is_contiguous() && out.stride(1) == 1, "moe_combine: layouts");
+  TORCH_CHECK(y.stride(1) == 1 && y.stride(0) >= out.size(1) && out.stride(1) == 1, "moe_combine: layouts");
   const c10::cuda::CUDAGuard guard(y.device());
   const __nv_bfloat16* b = nullptr;
   if (bias.has_value()) {
@@ -1168,7 +1168,7 @@ void moe_combine(const at::Tensor& y, const at::Tensor& inv_pos, const at::Tenso
                            shared.has_value() ? shared->stride(0) : 0,
                            shared_gate.has_value() ? shared_gate->data_ptr<float>() : nullptr,
                            reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0),
-                           cur_stream());
+                           cur_stream(), y.stride(0));
   check_launch("moe_combine", T > 0 ? 1 : 0);
 }
 

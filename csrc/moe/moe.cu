@@ -359,7 +359,7 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y,
                                    const __nv_bfloat16* __restrict__ bias, int e_start, int k,
                                    int H, const __nv_bfloat16* __restrict__ shared,
                                    long long ld_shared, const float* __restrict__ shared_gate,
-                                   __nv_bfloat16* __restrict__ out, long long ldo) {
+                                   __nv_bfloat16* __restrict__ out, long long ldo, long long ldy) {
   pdl_trigger();
   pdl_wait();
   const int t = blockIdx.x;
@@ -384,7 +384,7 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y,
       const int pos = inv_pos[(long long)t * k + j];
       if (pos < 0) continue;
       const float wt = weights[(long long)t * k + j];
-      const uint4 u = *reinterpret_cast<const uint4*>(y + (long long)pos * H + c);
+      const uint4 u = *reinterpret_cast<const uint4*>(y + (long long)pos * ldy + c);
       const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
       float v[8];
 #pragma unroll
@@ -473,12 +473,13 @@ void moe_combine_launch(const __nv_bfloat16* y, const int* inv_pos, const float*
                         const int* ids, const __nv_bfloat16* bias, int e_start, int T, int k,
                         int H, const __nv_bfloat16* shared, long long ld_shared,
                         const float* shared_gate, __nv_bfloat16* out, long long ldo,
-                        cudaStream_t s) {
+                        cudaStream_t s, long long ldy) {
   if (T == 0) return;
-  if (H % 8 != 0 || ldo % 8 != 0 || (shared != nullptr && ld_shared % 8 != 0))
+  if (ldy == 0) ldy = H;
+  if (H % 8 != 0 || ldo % 8 != 0 || ldy % 8 != 0 || ldy < H || (shared != nullptr && ld_shared % 8 != 0))
     throw std::invalid_argument("moe_combine: hidden size and strides must be multiples of 8");
   launch_pdl(moe_combine_kernel, dim3(T), dim3(256), 0, s, y, inv_pos, weights, ids, bias, e_start,
-             k, H, shared, ld_shared, shared_gate, out, ldo);
+             k, H, shared, ld_shared, shared_gate, out, ldo, ldy);
 }
 
 }  // namespace b200

@@ -51,7 +51,7 @@ void moe_combine_launch(const __nv_bfloat16* y, const int* inv_pos, const float*
                         const int* ids, const __nv_bfloat16* bias, int e_start, int T, int k,
                         int H, const __nv_bfloat16* shared, long long ld_shared,
                         const float* shared_gate, __nv_bfloat16* out, long long ldo,
-                        cudaStream_t s);
+                        cudaStream_t s, long long ldy = 0);
 
 // Y[rows, N] = X[rows, K] @ dequant(W_e)^T for the tile list of moe_align (<= 16 rows per pass),
 // W in MXFP4 tiles (moe_mxfp4.cu): wt [E, ceil(N / 256), K / 64, tile_bytes] uint8.

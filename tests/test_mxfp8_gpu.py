@@ -96,3 +96,31 @@ def test_mx8_grouped_experts(cuda_device, T):
     assert _rel(out, ref) < 4e-2
     # against the unquantized activations too (both roundings)
     assert _rel(out, MO.experts_ref(x.float(), ids, w, wgu, wd)) < 8e-2
+
+
+@pytest.mark.parametrize("T", [5, 200])
+def test_mx8_padded_gptoss_experts(cuda_device, T):
+    """GPT-OSS-style experts (hidden and FFN not multiples of 128, biases, clamped SwiGLU): the
+    MXFP4 stacks re-encoded losslessly as MXFP8 with K and the down projection's rows zero-padded
+    to 128s; the padded output rows are dropped by the combine (row stride above H)."""
+    from vllm_neuron_b200.models.gpt_oss import _quant_experts
+    from vllm_neuron_b200.ops import moe as MO
+
+    E, H, I, k = 4, 320, 192, 2
+    g = torch.Generator(device="cpu").manual_seed(T + 11)
+    gb, gs = _quant_experts((torch.randn(E, 2 * I, H, generator=g) * 0.05).to(cuda_device))
+    db, ds = _quant_experts((torch.randn(E, H, I, generator=g) * 0.05).to(cuda_device))
+    w4gu, w4d = L.MXFP4Weight.from_blocks(gb, gs), L.MXFP4Weight.from_blocks(db, ds)
+    wgu = L.MXFP8Weight.from_mxfp4(w4gu, k_pad=384)
+    wd = L.MXFP8Weight.from_mxfp4(w4d, k_pad=256, n_pad=384)
+    assert torch.equal(wgu.dequant()[..., :H], w4gu.dequant_bf16_ref().float())  # lossless
+    b_gu = (torch.randn(E, 2 * I, generator=g) * 0.1).to(cuda_device, torch.bfloat16)
+    b_dn = (torch.randn(E, H, generator=g) * 0.1).to(cuda_device, torch.bfloat16)
+    x = torch.randn(T, H, generator=g).to(cuda_device, torch.bfloat16)
+    ids = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)]).to(cuda_device, torch.int32)
+    w = torch.rand(T, k, generator=g).to(cuda_device)
+    out = MO.moe_experts(x, ids, w, wgu, wd, b_gu=b_gu, b_down=b_dn, act=MO.ACT_GPTOSS)
+    torch.cuda.synchronize()
+    xq, xs = L.quantize_mx8(x.float())
+    ref = MO.experts_ref(L.dequantize_mx8(xq, xs), ids, w, w4gu, w4d, b_gu, b_dn, act=MO.ACT_GPTOSS)
+    assert _rel(out, ref) < 4e-2

@@ -135,6 +135,28 @@ class GptOssForCausalLM(MoEMixin, LlamaForCausalLM):
         if dev.type == "cuda":
             torch.cuda.empty_cache()
 
+    @torch.no_grad()
+    def quantize_mxfp8(self) -> int:
+        """MXFP8 experts on the block-scaled tensor cores: each MXFP4 expert stack is re-encoded
+        losslessly as MXFP8 (e2m1 values are e4m3 values, the e8m0 scales carry over), zero-padded
+        to K in 128s and 128-row experts (hidden 2880 -> 2944), and served W8A8 by the grouped
+        GEMM with the expert-sorted activations quantized to MXFP8; the fp4 decode copies are
+        dropped.  Dense projections whose K is a multiple of 128 become MXFP8 as well."""
+        n = super().quantize_mxfp8()
+        rup = lambda v: -(-v // 128) * 128
+        for ly in self.layers:
+            if not isinstance(ly.w_gu, L.MXFP4Weight):
+                continue
+            gu = L.MXFP8Weight.from_mxfp4(ly.w_gu, k_pad=rup(self.H))
+            dn = L.MXFP8Weight.from_mxfp4(ly.w_down, k_pad=rup(self.I_moe), n_pad=rup(self.H))
+            ly.w_gu, ly.w_down = gu, dn
+            ly.fp4_gu = ly.fp4_down = None
+            n += 2
+        self.mx_linears = n
+        if self.device.type == "cuda":
+            torch.cuda.empty_cache()
+        return n
+
     def _mlp(self, i, ly, x, res, nxt_norm, T, small, fused):
         h = self.ws_h[:T]
         if self.a2a is not None:

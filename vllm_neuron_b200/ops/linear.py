@@ -189,6 +189,23 @@ class MXFP8Weight:
         q, s = quantize_mx8(w.detach())
         return cls(q, s)
 
+    @classmethod
+    def from_mxfp4(cls, w: "MXFP4Weight", k_pad: int | None = None, n_pad: int | None = None) -> "MXFP8Weight":
+        """Lossless re-encoding of an MXFP4 weight (every e2m1 value is an e4m3 value; the e8m0
+        scales carry over), optionally padded with zeros to ``k_pad`` columns and ``n_pad`` rows
+        (the grouped block-scaled GEMM wants K in 128s and 128-row experts)."""
+        lut = torch.tensor(FP4_VALUES, dtype=torch.float32, device=w.q.device)
+        lo, hi = (w.q & 0xF).long(), (w.q >> 4).long()
+        vals = torch.stack([lut[lo], lut[hi]], dim=-1).flatten(-2)  # [..., N, K]
+        *lead, N, K = vals.shape
+        kp, np_ = k_pad or K, n_pad or N
+        assert kp >= K and kp % 128 == 0 and np_ >= N
+        q = torch.zeros(*lead, np_, kp, dtype=torch.float8_e4m3fn, device=w.q.device)
+        q[..., :N, :K] = vals.to(torch.float8_e4m3fn)
+        sc = torch.full((*lead, np_, kp // 32), 127, dtype=torch.uint8, device=w.q.device)
+        sc[..., :N, :K // 32] = w.scales
+        return cls(q, sc)
+
     @property
     def shape(self):
         return self.q.shape

@@ -328,6 +328,17 @@ class _MX8TileBufs:
                                     torch.zeros(n, K // 128, 512, dtype=torch.uint8, device=device))
         return cur[0][:rows], cur[1]
 
+    @classmethod
+    def out(cls, rows: int, N: int, device) -> torch.Tensor:
+        """bf16 output rows of a row-padded expert stack (the combine reads the first H columns)."""
+        key = ("out", str(device), N)
+        cur = cls.cache.get(key)
+        if cur is None or cur.shape[0] < rows:
+            if cur is not None:
+                cls.retired.append(cur)
+            cur = cls.cache[key] = torch.empty(max(rows, 128), N, dtype=torch.bfloat16, device=device)
+        return cur[:rows]
+
 
 def _mx8_experts_ok(w_gu, w_down) -> bool:
     return (isinstance(w_gu, L.MXFP8Weight) and isinstance(w_down, L.MXFP8Weight)
@@ -348,11 +359,12 @@ def _experts_cuda(x, ids, w, w_gu, w_down, k, b_gu, b_down, act, alpha, limit, e
         # MXFP8 experts on the block-scaled tensor cores: the sorted rows are quantized to MXFP8
         # with one scale atom per tile-list entry; decode-size batches swap operands (expert
         # weight rows as the 128-row operand, each expert's <= 64 tokens as the N tile)
+        # (stacks may be zero-padded: K to 128s, the down projection's rows to 128-row experts)
         gmax = ws.gtiles.shape[0]
         swap = T <= SWAP_MAX_TOKENS
         bn_t = L.skinny_bn(T) if swap else 0
         gt = ws.gtiles[:min(gmax, R)] if swap else ws.gtiles
-        xq, sfx = _MX8TileBufs.get(R, H, gmax, x.device)
+        xq, sfx = _MX8TileBufs.get(R, w_gu.q.shape[-1], gmax, x.device)
         ext().quant_mx8_tiles(xp, xq, sfx, ws.gtiles, ws.gcount)
         gu = ws.gu[:R]
         if swap:
@@ -361,9 +373,10 @@ def _experts_cuda(x, ids, w, w_gu, w_down, k, b_gu, b_down, act, alpha, limit, e
             ext().gemm_mx8_grouped(xq, w_gu.q, gu, EPI_BF16, 128, sfx, w_gu.sf, gt, ws.gcount, 0)
         a = ws.act[:R, :I]
         ext().moe_act(gu, b_gu, ws.row_expert, ws.offsets, act, alpha, limit, a)
-        aq, sfa = _MX8TileBufs.get(R, I, gmax, x.device)
+        aq, sfa = _MX8TileBufs.get(R, w_down.q.shape[-1], gmax, x.device)
         ext().quant_mx8_tiles(a, aq, sfa, ws.gtiles, ws.gcount)
-        y = ws.y[:R]
+        nd = w_down.q.shape[1]
+        y = ws.y[:R] if nd == H else _MX8TileBufs.out(R, nd, x.device)
         if swap:
             ext().gemm_mx8_grouped(w_down.q, aq, y, EPI_BF16_T, bn_t, w_down.sf, sfa, gt, ws.gcount, 1)
         else:
