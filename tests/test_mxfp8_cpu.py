@@ -108,3 +108,16 @@ def test_mxfp8_checkpoint_loads_exactly_and_serves_mx():
     got = mx.engine.prompt_logits(prompts)
     rel = float((got - exact).norm() / exact.norm())
     assert rel < 0.05, rel  # the activations' MXFP8 rounding only
+
+
+def test_mxfp4_reencodes_losslessly_with_padding():
+    from vllm_neuron_b200.models.gpt_oss import _quant_experts
+
+    g = torch.Generator().manual_seed(5)
+    b, s = _quant_experts(torch.randn(3, 96, 320, generator=g) * 0.1)
+    w4 = L.MXFP4Weight.from_blocks(b, s)
+    w8 = L.MXFP8Weight.from_mxfp4(w4, k_pad=384, n_pad=128)
+    assert w8.q.shape == (3, 128, 384) and w8.sf.shape == (3, 3, 512)
+    d8 = w8.dequant()
+    assert torch.equal(d8[:, :96, :320], w4.dequant_bf16_ref().float())
+    assert d8[:, 96:].abs().sum() == 0 and d8[:, :, 320:].abs().sum() == 0
