@@ -126,3 +126,57 @@ def test_tp2_matches_tp1(ckpt, fused, sp, sdp):
     # the generated tokens to match.
     same = sum(a == b for r, g2 in zip(ref, got) for a, b in zip(r, g2))
     assert same >= 0.8 * sum(len(r) for r in ref), (ref, got)
+
+
+ADP_WORKER = r'''
+import json, os, sys, torch
+sys.path.insert(0, sys.argv[1])
+from vllm_neuron_b200.entrypoints import LLM
+from vllm_neuron_b200.engine.sampling_params import SamplingParams
+ckpt, out_path = sys.argv[2], sys.argv[3]
+torch.cuda.set_device(int(os.environ["LOCAL_RANK"]))
+W = int(os.environ["WORLD_SIZE"])
+llm = LLM(ckpt, tensor_parallel_size=W, max_num_seqs=8, max_model_len=256, num_gpu_blocks=256,
+          max_num_batched_tokens=256, skip_tokenizer_init=True,
+          additional_config={"neuron_config": {"attention_dp_size": W}})
+m = llm.engine.model
+assert m.adp is not None and m.mlp_tp.world == W and m.tp.world == 1
+g = torch.Generator().manual_seed(0)
+prompts = [torch.randint(0, 32000, (40,), generator=g).tolist() for _ in range(6)]
+sps = [SamplingParams(temperature=0, max_tokens=n, ignore_eos=True) for n in [12, 5, 9, 12, 3, 7]]
+outs = llm.generate(prompts, sps)
+if int(os.environ["RANK"]) == 0:
+    json.dump([o.outputs[0].token_ids for o in outs], open(out_path, "w"))
+import torch.distributed as dist
+dist.barrier(); dist.destroy_process_group()
+'''
+
+
+def test_attention_dp2_matches_tp1(ckpt):
+    """Attention DP over 2 GPUs: each GPU a replica running attention on its own requests, the
+    MLP sharded over both with an NCCL all-gather / all-reduce per layer."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from vllm_neuron_b200.engine.sampling_params import SamplingParams
+    from vllm_neuron_b200.entrypoints import LLM
+
+    g = torch.Generator().manual_seed(0)
+    prompts = [torch.randint(0, 32000, (40,), generator=g).tolist() for _ in range(6)]
+    sps = [SamplingParams(temperature=0, max_tokens=n, ignore_eos=True) for n in [12, 5, 9, 12, 3, 7]]
+    llm = LLM(ckpt, max_num_seqs=8, max_model_len=256, num_gpu_blocks=256, max_num_batched_tokens=256,
+              skip_tokenizer_init=True)
+    ref = [o.outputs[0].token_ids for o in llm.generate(prompts, sps)]
+    llm.shutdown()
+    out = tempfile.mktemp(suffix=".json")
+    script = tempfile.mktemp(suffix=".py")
+    with open(script, "w") as f:
+        f.write(ADP_WORKER)
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr=127.0.0.1", f"--master-port={_port()}", script, ROOT, ckpt, out]
+    r = subprocess.run(["timeout", "-k", "30", "300"] + cmd, env=env, capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    got = json.load(open(out))
+    assert [len(x) for x in got] == [len(x) for x in ref]
+    same = sum(a == b for r1, g2 in zip(ref, got) for a, b in zip(r1, g2))
+    assert same >= 0.8 * sum(len(x) for x in ref), (ref, got)

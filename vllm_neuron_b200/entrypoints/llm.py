@@ -65,6 +65,16 @@ class LLM:
             device = f"cuda:{torch.cuda.current_device()}" if torch.cuda.is_available() else "cpu"
         ps.init_distributed(backend="gloo" if str(device).startswith("cpu") else None)
         world = torch.distributed.get_world_size() if torch.distributed.is_initialized() else 1
+        adp = int(_b200_opts(additional_config).get("attention_dp_size", 1) or 1)
+        if adp > 1:
+            # attention data parallelism: the TP world splits into adp replicas that each run
+            # attention over tensor_parallel_size / adp ranks on their own requests; the MLP
+            # stays sharded over all tensor_parallel_size ranks
+            if world != tensor_parallel_size or tensor_parallel_size % adp or data_parallel_size not in (None, 1, adp):
+                raise ValueError(f"attention_dp_size={adp} needs the launched world ({world}) to equal "
+                                 f"tensor_parallel_size ({tensor_parallel_size}), divisible by it")
+            tensor_parallel_size //= adp
+            data_parallel_size = adp
         if world % tensor_parallel_size:
             raise ValueError(f"tensor_parallel_size={tensor_parallel_size} does not divide the {world} launched ranks")
         dp = world // tensor_parallel_size
@@ -75,6 +85,7 @@ class LLM:
                                                             tensor_parallel_size=tensor_parallel_size,
                                                             data_parallel_size=dp,
                                                             decode_context_parallel_size=decode_context_parallel_size,
+                                                            attention_dp_size=adp,
                                                             vision_tp_size=vision_tp_of(additional_config)))
         # Data parallelism: each group of TP ranks is an independent engine replica serving
         # every dp-th request; outputs are gathered over the DP group (reference: data
@@ -141,7 +152,7 @@ class LLM:
 
     def _generate_dp(self, prompts, sampling_params) -> list[RequestOutput]:
         mine = [i for i in range(len(prompts)) if i % self.dp_size == self.dp_rank]
-        if getattr(self.engine.model, "a2a", None) is not None:
+        if getattr(self.engine.model, "a2a", None) is not None or getattr(self.engine.model, "adp", None) is not None:
             # replicas share the MoE layers' all-to-alls: step in lockstep, idle ones run a
             # one-token dummy forward (reference: DP dummy batch, neuron_model_runner.py:7710)
             local = self._generate([prompts[i] for i in mine], [sampling_params[i] for i in mine],

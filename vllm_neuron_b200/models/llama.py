@@ -136,6 +136,11 @@ class LlamaForCausalLM(torch.nn.Module):
         self.aux_hidden: torch.Tensor | None = None
         # accuracy tooling: activation capture / golden replacement (accuracy.tensor_capture)
         self.capture = None
+        # attention data parallelism (set_attention_dp): replica group of the attention and the
+        # MLP's tensor-parallel group over all replicas; rows each replica contributes this step
+        self.adp = None
+        self.mlp_tp = None
+        self.adp_tmax = 1
 
     # ---------------------------------------------------------------- init / weights
     def _make_attn(self, m, p, layer: int):
@@ -531,6 +536,8 @@ class LlamaForCausalLM(torch.nn.Module):
 
     def _mlp(self, i: int, ly, x, res, nxt_norm, T: int, small: bool, fused: bool):
         """Dense SwiGLU MLP; leaves ``x = nxt_norm(res += mlp(x))``."""
+        if self.adp is not None:
+            return self._mlp_adp(ly, x, res, nxt_norm, T)
         if small:
             acc = self.acc_gu[:T]
             L.gemm_accumulate(x, ly.gate_up, acc)
@@ -555,6 +562,49 @@ class LlamaForCausalLM(torch.nn.Module):
                 act = ops.silu_mul(gu, out=self.ws_act[:T])
             h = L.gemm_out(act, ly.down, out=self.ws_h[:T])
             self._reduce_norm(h, res, nxt_norm, x)
+
+    def set_attention_dp(self, adp: GroupComm, mlp_tp: GroupComm):
+        """Attention data parallelism: this model's ``tp`` group runs attention (heads sharded
+        over it, KV cache of its own requests only), ``adp`` holds the ranks at the same TP
+        position in the other replicas, and the dense MLP is sharded over ``mlp_tp`` (every rank
+        of every replica).  Each layer gathers the replicas' normalised rows over ``adp``
+        (padded to the step's largest replica batch, ``adp_tmax``), runs the MLP shard on all of
+        them, all-reduces over ``mlp_tp`` and keeps its own rows.  Must be called before the
+        weights are loaded.  Reference: attention DP ("KVDP") with the attention / MLP DP
+        transitions, vllm_neuron/model/llama3/model.py:341-408,1125-1157 and
+        vllm_neuron/parallel/neuron_parallel_state.py:593-617."""
+        if type(self)._mlp is not LlamaForCausalLM._mlp:
+            raise NotImplementedError(f"attention data parallelism: {type(self).__name__} has no dense MLP")
+        if self.cfg.intermediate_size % mlp_tp.world:
+            raise ValueError(f"the MLP width {self.cfg.intermediate_size} does not split over {mlp_tp.world} ranks")
+        self.adp, self.mlp_tp = adp, mlp_tp
+        self.I = self.cfg.intermediate_size // mlp_tp.world
+        self.silu_blk = L.SILU_BLOCK if self.I % L.SILU_BLOCK == 0 else 0
+        p = lambda *s: torch.nn.Parameter(torch.empty(*s, dtype=self.dtype, device=self.device), requires_grad=False)
+        for i, ly in enumerate(self.layers):
+            self._make_mlp(ly, p, i)
+        self.ws_act = torch.zeros(self.ws_act.shape[0], self.I, dtype=self.dtype, device=self.device)
+        self.acc_gu = torch.zeros(self.acc_gu.shape[0], 2 * self.I, dtype=torch.float32, device=self.device)
+
+    def _mlp_adp(self, ly, x, res, nxt_norm, T: int):
+        """MLP of attention data parallelism: gather the replicas' rows, run this rank's MLP
+        shard on all of them, all-reduce over every rank, keep this replica's rows."""
+        D, Tm, H = self.adp.world, max(self.adp_tmax, T, 1), self.H
+        xp = x.new_zeros(Tm, H)
+        xp[:T] = x[:T]
+        xall = self.adp.all_gather(xp.unsqueeze(0).contiguous(), dim=0).reshape(D * Tm, H)
+        if self.silu_blk:
+            act = L.gemm_silu(xall, ly.gate_up)
+        else:
+            act = ops.silu_mul(L.gemm_out(xall, ly.gate_up))
+        h = L.gemm_out(act, ly.down)
+        self.mlp_tp.all_reduce_(h)
+        r = self.adp.rank
+        self._add_norm_rows(h[r * Tm:r * Tm + T], res, nxt_norm, x, T)
+
+    def _add_norm_rows(self, h, res, norm_w, x, T: int):
+        """``res[:T] += h``, ``x[:T] = rmsnorm(res[:T])`` (h already reduced)."""
+        ops.add_rmsnorm(h.contiguous(), res[:T], norm_w, self.eps, out=x[:T])
 
     def _allreduce_norm(self, acc, res, norm_w, x, fused: bool):
         """Decode-size row-parallel epilogue: ``res += all_reduce(acc)``, ``x = rmsnorm(res)``."""

@@ -93,8 +93,9 @@ class ParallelConfig:
             raise ValueError("DCP size must divide TP")
         if self.tensor_parallel_size % self.vision_tp_size:
             raise ValueError("vision_tp_size must divide TP")
-        if self.tensor_parallel_size % self.attention_dp_size:
-            raise ValueError("attention_dp_size must divide TP")
+        if self.attention_dp_size > 1 and self.attention_dp_size != self.data_parallel_size:
+            raise ValueError("attention data parallelism runs one replica per attention-DP rank "
+                             "(data_parallel_size == attention_dp_size)")
         ep = self.expert_parallel_size or self.world_size
         if self.world_size % ep:
             raise ValueError("EP size must divide the world size")
@@ -109,6 +110,7 @@ class ParallelState:
     ep: GroupComm = field(default_factory=lambda: GroupComm(None))
     dcp: GroupComm = field(default_factory=lambda: GroupComm(None))
     vision_tp: GroupComm = field(default_factory=lambda: GroupComm(None))
+    world: GroupComm = field(default_factory=lambda: GroupComm(None))  # attention DP: the MLP group
     cpu: dist.ProcessGroup | None = None
     dp_cpu: dist.ProcessGroup | None = None   # gloo group of this rank's DP peers
     groups: dict = field(default_factory=dict)
@@ -172,6 +174,8 @@ def initialize_parallel_state(cfg: ParallelConfig) -> ParallelState:
         for g in tp_groups(W, tp):
             sets.extend(sub_groups(g, cfg.vision_tp_size)[0])
         st.vision_tp, _ = _make(sets, rank)
+    if cfg.attention_dp_size > 1:
+        st.world, _ = _make([list(range(W))], rank)
     st.cpu = dist.new_group(list(range(W)), backend="gloo")
     if W // tp > 1:
         for g in dp_groups(W, tp):

@@ -99,8 +99,10 @@ def load_dense_decoder(model, get_tensor: Callable[[str], torch.Tensor], names: 
 
 def load_dense_mlp(model, ly, get_tensor, p: str):
     """SwiGLU MLP of one layer: gate/up rows sharded (and block-interleaved for the fused SiLU
-    epilogue), down columns sharded."""
-    W, r = model.tp.world, model.tp.rank
+    epilogue), down columns sharded (over the MLP group of attention data parallelism, else
+    over TP)."""
+    mg = getattr(model, "mlp_tp", None) or model.tp
+    W, r = mg.world, mg.rank
     g = shard_rows(get_tensor(p + "mlp.gate_proj.weight"), W, r)
     u = shard_rows(get_tensor(p + "mlp.up_proj.weight"), W, r)
     gu = L.interleave_gate_up(g, u) if model.silu_blk else torch.cat([g, u], 0)
