@@ -136,11 +136,12 @@ from vllm_neuron_b200.engine.sampling_params import SamplingParams
 ckpt, out_path = sys.argv[2], sys.argv[3]
 torch.cuda.set_device(int(os.environ["LOCAL_RANK"]))
 W = int(os.environ["WORLD_SIZE"])
-llm = LLM(ckpt, tensor_parallel_size=W, max_num_seqs=8, max_model_len=256, num_gpu_blocks=256,
+llm = LLM(ckpt, tensor_parallel_size=1, max_num_seqs=8, max_model_len=256, num_gpu_blocks=256,
           max_num_batched_tokens=256, skip_tokenizer_init=True,
-          additional_config={"neuron_config": {"attention_dp_size": W}})
+          additional_config={"neuron_config": {"mlp_dp_size": W, "embedding_dp_size": W, "lm_head_dp_size": W,
+                                               "attention_dp_size": W}})
 m = llm.engine.model
-assert m.adp is not None and m.mlp_tp.world == W and m.tp.world == 1
+assert m.cdp_mlp and m.cdp_embed and m.cdp_lmh and m.cdp_attn and m.comp_tp.world == W and m.tp.world == 1
 g = torch.Generator().manual_seed(0)
 prompts = [torch.randint(0, 32000, (40,), generator=g).tolist() for _ in range(6)]
 sps = [SamplingParams(temperature=0, max_tokens=n, ignore_eos=True) for n in [12, 5, 9, 12, 3, 7]]
@@ -152,9 +153,11 @@ dist.barrier(); dist.destroy_process_group()
 '''
 
 
-def test_attention_dp2_matches_tp1(ckpt):
-    """Attention DP over 2 GPUs: each GPU a replica running attention on its own requests, the
-    MLP sharded over both with an NCCL all-gather / all-reduce per layer."""
+def test_component_dp2_matches_tp1(ckpt):
+    """Component and attention DP over 2 GPUs: each GPU a data-parallel replica with the KV cache
+    of its own requests; the MLP, the embedding, the LM head and the Q / O heads sharded over
+    both GPUs (NCCL all-gathers of the replicas' rows, all-to-alls around attention,
+    all-reduces)."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     from vllm_neuron_b200.engine.sampling_params import SamplingParams
@@ -178,5 +181,9 @@ def test_attention_dp2_matches_tp1(ckpt):
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     got = json.load(open(out))
     assert [len(x) for x in got] == [len(x) for x in ref]
+    # the first token of every request is the argmax of its prefill logits; afterwards bf16 sums
+    # in a different order (MLP partials over two GPUs, vocab-sliced LM head) may swap near ties
+    # of this random model and a sequence then follows another path
+    assert [x[0] for x in got] == [x[0] for x in ref], (ref, got)
     same = sum(a == b for r1, g2 in zip(ref, got) for a, b in zip(r1, g2))
-    assert same >= 0.8 * sum(len(x) for x in ref), (ref, got)
+    assert same >= 0.7 * sum(len(x) for x in ref), (ref, got)

@@ -249,11 +249,6 @@ class B200Config:
             raise ValueError(f"unknown quantization {self.quantization!r}")
         # Options of the reference this framework does not implement are refused rather than
         # silently ignored, so a migrated configuration never changes meaning quietly.
-        for name in ("embedding_dp_size", "lm_head_dp_size", "mlp_dp_size"):
-            if getattr(self, name) > 1:
-                raise NotImplementedError(
-                    f"{name}={getattr(self, name)}: component data parallelism is not implemented; "
-                    "the embedding, MLP and LM head run tensor parallel over the whole TP group")
         if self.fp8_packed_kv:
             raise NotImplementedError("fp8_packed_kv: the packed FP8 K layout is not implemented; "
                                       "use kv_cache_dtype='fp8' (e4m3 K/V, unpacked)")

@@ -114,21 +114,26 @@ def build_model(args: EngineArgs, tp: GroupComm = SINGLE):
             raise ValueError(f"vision tp_size {vcfg.tp_size} does not match the vision TP group "
                              f"({model.visual.tp.world} ranks)")
         model.configure_vision(vcfg, cuda_graphs=b200_config.cuda_graphs)
-    if b200_config.attention_dp_size > 1:
-        # attention data parallelism (the front end made one replica per attention-DP rank):
-        # the MLP is re-sharded over every rank before the weights load; replicas step in
+    cdp = {k: getattr(b200_config, k) > 1 for k in ("mlp_dp_size", "embedding_dp_size", "lm_head_dp_size",
+                                                    "attention_dp_size")}
+    if any(cdp.values()):
+        # component / attention data parallelism (the front end made the replicas and the
+        # TP x DP group): re-shard the components before the weights load; replicas step in
         # lockstep and run eagerly (their batch sizes differ per step)
         from ..parallel import state as _ps
 
         st = _ps.get_parallel_state()
-        if st.config.attention_dp_size != b200_config.attention_dp_size:
-            raise ValueError("attention_dp_size must be passed to the LLM front end (the parallel state "
-                             "has no attention-DP groups)")
-        if not hasattr(model, "set_attention_dp"):
-            raise NotImplementedError(f"{type(model).__name__} does not support attention data parallelism")
-        model.set_attention_dp(st.dp, st.world)
+        if not st.config.component_dp:
+            raise ValueError("component DP sizes must be passed to the LLM front end (no TP x DP group)")
+        if not hasattr(model, "set_component_dp"):
+            raise NotImplementedError(f"{type(model).__name__} does not support component data parallelism")
+        model.set_component_dp(st.dp, st.world, mlp=cdp["mlp_dp_size"], embed=cdp["embedding_dp_size"],
+                               lm_head=cdp["lm_head_dp_size"])
+        if cdp["attention_dp_size"]:
+            model.set_attention_dp()
         b200_config.cuda_graphs = False
         b200_config.sequence_parallel = False
+        b200_config.sampling_dp = False
     ck_info = {}
     if args.load_format == "dummy" or model_path is None:
         model.init_random(seed=args.seed)
@@ -433,8 +438,8 @@ class LLMEngine:
         """Logits of the last prompt position of each prompt (one prefill step, nothing is
         sampled or kept): the hook of the logit-validation tooling.  Returns ``[N, V]`` fp32 on
         the CPU.  Must be called with no requests in flight."""
-        if getattr(self.model, "adp", None) is not None:
-            raise NotImplementedError("prompt_logits: attention-DP replicas only step in lockstep (generate)")
+        if getattr(self.model, "dpcol", None) is not None:
+            raise NotImplementedError("prompt_logits: component-DP replicas only step in lockstep (generate)")
         from .scheduler import ScheduledRequest, SchedulerOutput
 
         if self.has_unfinished_requests():
@@ -709,8 +714,8 @@ class LLMEngine:
     def run_lockstep(self, group) -> list[Request]:
         """Serve this replica's requests in lockstep with the other data-parallel replicas of
         ``group`` (gloo): every iteration all replicas agree (MAX all-reduce of two flags and the
-        batch size) on whether any of them has a batch and on the largest batch (the row padding
-        of attention data parallelism); a replica with nothing scheduled then runs a one-token
+        batch sizes) on whether any of them has a batch and on the largest batch (the row padding
+        of component data parallelism); a replica with nothing scheduled then runs a one-token
         dummy forward so that the collectives inside the model (all-to-all expert exchange)
         match.  Synchronous scheduling only.  Reference: the DP padding all-reduce and dummy
         batch (vllm_neuron/vllm/worker/neuron_model_runner.py:7337-7489, 7710)."""
@@ -720,10 +725,13 @@ class LLMEngine:
         while True:
             out = self.scheduler.schedule()
             flags = torch.tensor([0 if out.empty else 1, 1 if self.scheduler.has_unfinished() else 0,
-                                  0 if out.empty else out.num_tokens], dtype=torch.int64)
+                                  0 if out.empty else out.num_tokens,
+                                  0 if out.empty else sum(s.num_logits for s in out.scheduled)],
+                                 dtype=torch.int64)
             dist.all_reduce(flags, op=dist.ReduceOp.MAX, group=group)
-            # attention data parallelism: every replica pads its rows to the largest batch
-            self.model.adp_tmax = max(1, int(flags[2]))
+            # component data parallelism: every replica pads its rows to the largest batch
+            self.model.dp_tmax = max(1, int(flags[2]))
+            self.model.dp_smax = max(1, int(flags[3]))
             if flags[0] == 0:
                 if flags[1] == 0:
                     return done

@@ -65,27 +65,27 @@ class LLM:
             device = f"cuda:{torch.cuda.current_device()}" if torch.cuda.is_available() else "cpu"
         ps.init_distributed(backend="gloo" if str(device).startswith("cpu") else None)
         world = torch.distributed.get_world_size() if torch.distributed.is_initialized() else 1
-        adp = int(_b200_opts(additional_config).get("attention_dp_size", 1) or 1)
-        if adp > 1:
-            # attention data parallelism: the TP world splits into adp replicas that each run
-            # attention over tensor_parallel_size / adp ranks on their own requests; the MLP
-            # stays sharded over all tensor_parallel_size ranks
-            if world != tensor_parallel_size or tensor_parallel_size % adp or data_parallel_size not in (None, 1, adp):
-                raise ValueError(f"attention_dp_size={adp} needs the launched world ({world}) to equal "
-                                 f"tensor_parallel_size ({tensor_parallel_size}), divisible by it")
-            tensor_parallel_size //= adp
-            data_parallel_size = adp
         if world % tensor_parallel_size:
             raise ValueError(f"tensor_parallel_size={tensor_parallel_size} does not divide the {world} launched ranks")
         dp = world // tensor_parallel_size
         if data_parallel_size not in (None, dp):
             raise ValueError(f"data_parallel_size={data_parallel_size} but TP={tensor_parallel_size} x "
                              f"{world} ranks give {dp}")
+        opts = _b200_opts(additional_config)
+        # component / attention data parallelism: embedding / MLP / LM head / Q-O heads sharded
+        # over TP x DP ranks (all replicas), which then step in lockstep
+        cdp = {k: int(opts.get(k, 1) or 1) for k in ("embedding_dp_size", "mlp_dp_size", "lm_head_dp_size",
+                                                      "attention_dp_size")}
+        for k, v in cdp.items():
+            if v > 1 and v != dp:
+                raise NotImplementedError(f"{k}={v}: component data parallelism spans every data-parallel "
+                                          f"replica ({k} = data_parallel_size = {dp})")
         st = ps.initialize_parallel_state(ps.ParallelConfig(world_size=world,
                                                             tensor_parallel_size=tensor_parallel_size,
                                                             data_parallel_size=dp,
                                                             decode_context_parallel_size=decode_context_parallel_size,
-                                                            attention_dp_size=adp,
+                                                            component_dp=any(v > 1 for v in cdp.values()),
+                                                            attention_dp_size=cdp["attention_dp_size"],
                                                             vision_tp_size=vision_tp_of(additional_config)))
         # Data parallelism: each group of TP ranks is an independent engine replica serving
         # every dp-th request; outputs are gathered over the DP group (reference: data
@@ -152,7 +152,7 @@ class LLM:
 
     def _generate_dp(self, prompts, sampling_params) -> list[RequestOutput]:
         mine = [i for i in range(len(prompts)) if i % self.dp_size == self.dp_rank]
-        if getattr(self.engine.model, "a2a", None) is not None or getattr(self.engine.model, "adp", None) is not None:
+        if getattr(self.engine.model, "a2a", None) is not None or getattr(self.engine.model, "dpcol", None) is not None:
             # replicas share the MoE layers' all-to-alls: step in lockstep, idle ones run a
             # one-token dummy forward (reference: DP dummy batch, neuron_model_runner.py:7710)
             local = self._generate([prompts[i] for i in mine], [sampling_params[i] for i in mine],

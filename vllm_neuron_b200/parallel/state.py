@@ -85,6 +85,7 @@ class ParallelConfig:
     decode_context_parallel_size: int = 1
     attention_dp_size: int = 1
     vision_tp_size: int = 1
+    component_dp: bool = False   # embedding / MLP / LM head sharded over every rank
 
     def validate(self):
         if self.tensor_parallel_size * self.data_parallel_size != self.world_size:
@@ -94,8 +95,9 @@ class ParallelConfig:
         if self.tensor_parallel_size % self.vision_tp_size:
             raise ValueError("vision_tp_size must divide TP")
         if self.attention_dp_size > 1 and self.attention_dp_size != self.data_parallel_size:
-            raise ValueError("attention data parallelism runs one replica per attention-DP rank "
-                             "(data_parallel_size == attention_dp_size)")
+            raise ValueError("attention_dp_size must equal the data-parallel size")
+        if self.component_dp and self.data_parallel_size < 2:
+            raise ValueError("component data parallelism needs data-parallel replicas")
         ep = self.expert_parallel_size or self.world_size
         if self.world_size % ep:
             raise ValueError("EP size must divide the world size")
@@ -110,7 +112,7 @@ class ParallelState:
     ep: GroupComm = field(default_factory=lambda: GroupComm(None))
     dcp: GroupComm = field(default_factory=lambda: GroupComm(None))
     vision_tp: GroupComm = field(default_factory=lambda: GroupComm(None))
-    world: GroupComm = field(default_factory=lambda: GroupComm(None))  # attention DP: the MLP group
+    world: GroupComm = field(default_factory=lambda: GroupComm(None))  # component DP: TP x DP ranks
     cpu: dist.ProcessGroup | None = None
     dp_cpu: dist.ProcessGroup | None = None   # gloo group of this rank's DP peers
     groups: dict = field(default_factory=dict)
@@ -174,7 +176,7 @@ def initialize_parallel_state(cfg: ParallelConfig) -> ParallelState:
         for g in tp_groups(W, tp):
             sets.extend(sub_groups(g, cfg.vision_tp_size)[0])
         st.vision_tp, _ = _make(sets, rank)
-    if cfg.attention_dp_size > 1:
+    if cfg.component_dp:
         st.world, _ = _make([list(range(W))], rank)
     st.cpu = dist.new_group(list(range(W)), backend="gloo")
     if W // tp > 1:

@@ -66,7 +66,13 @@ def load_dense_decoder(model, get_tensor: Callable[[str], torch.Tensor], names: 
     pre = "model." if any(n.startswith("model.") for n in names) else ""
     if any(n.startswith("model.language_model.") for n in names):
         pre = "model.language_model."
-    _copy(model.embed, shard_rows(get_tensor(pre + "embed_tokens.weight"), W, r, model.V_local), "embed")
+    # component data parallelism shards the embedding / LM head over every rank
+    cg = getattr(model, "comp_tp", None)
+    ew, er, ev = ((cg.world, cg.rank, model.V_local_emb) if getattr(model, "cdp_embed", False)
+                  else (W, r, model.V_local))
+    hw, hr, hv = ((cg.world, cg.rank, model.V_local_lmh) if getattr(model, "cdp_lmh", False)
+                  else (W, r, model.V_local))
+    _copy(model.embed, shard_rows(get_tensor(pre + "embed_tokens.weight"), ew, er, ev), "embed")
     for i, ly in enumerate(model.layers):
         p = f"{pre}layers.{i}."
         _copy(ly.input_norm, get_tensor(p + "input_layernorm.weight"), p + "input_layernorm")
@@ -74,6 +80,23 @@ def load_dense_decoder(model, get_tensor: Callable[[str], torch.Tensor], names: 
         q = get_tensor(p + "self_attn.q_proj.weight")
         k = get_tensor(p + "self_attn.k_proj.weight")
         v = get_tensor(p + "self_attn.v_proj.weight")
+        if getattr(model, "cdp_attn", False):
+            # attention data parallelism: Q / O heads of this (replica, TP position) sub-group,
+            # K / V of the replica's TP position
+            hq_w, dh = model.Hq_w, cfg.head_dim
+            h0 = r * (cfg.num_heads // W) + model.dpcol.rank * hq_w
+            _copy(ly.q_w, q[h0 * dh:(h0 + hq_w) * dh], p + "q_proj")
+            kv = fused_qkv(q, k, v, cfg.num_heads, cfg.num_kv_heads, dh, W, r)[model.Hq * dh:]
+            _copy(ly.kv, kv, p + "kv")
+            _copy(ly.o, get_tensor(p + "self_attn.o_proj.weight")[:, h0 * dh:(h0 + hq_w) * dh], p + "o_proj")
+            if ly.q_norm is not None:
+                _copy(ly.q_norm, get_tensor(p + "self_attn.q_norm.weight"), p + "q_norm")
+                _copy(ly.k_norm, get_tensor(p + "self_attn.k_norm.weight"), p + "k_norm")
+            if mlp_loader is not None:
+                mlp_loader(model, ly, get_tensor, names, p)
+            else:
+                load_dense_mlp(model, ly, get_tensor, p)
+            continue
         _copy(ly.qkv, fused_qkv(q, k, v, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, W, r), p + "qkv")
         if ly.qkv_bias is not None:
             qb = get_tensor(p + "self_attn.q_proj.bias")[:, None]
@@ -89,19 +112,21 @@ def load_dense_decoder(model, get_tensor: Callable[[str], torch.Tensor], names: 
             continue
         load_dense_mlp(model, ly, get_tensor, p)
     _copy(model.final_norm, get_tensor(pre + "norm.weight"), "norm")
-    if not cfg.tie_word_embeddings:
+    if getattr(model, "lm_head_from_embed", False):  # tied, but sharded differently
+        _copy(model.lm_head, shard_rows(get_tensor(pre + "embed_tokens.weight"), hw, hr, hv), "lm_head")
+    elif not cfg.tie_word_embeddings:
         head = "lm_head.weight"
         if head in names:
-            _copy(model.lm_head, shard_rows(get_tensor(head), W, r, model.V_local), "lm_head")
+            _copy(model.lm_head, shard_rows(get_tensor(head), hw, hr, hv), "lm_head")
         else:  # encoder-only checkpoints (embedding models) carry no LM head
             model.lm_head = model.embed
 
 
 def load_dense_mlp(model, ly, get_tensor, p: str):
     """SwiGLU MLP of one layer: gate/up rows sharded (and block-interleaved for the fused SiLU
-    epilogue), down columns sharded (over the MLP group of attention data parallelism, else
-    over TP)."""
-    mg = getattr(model, "mlp_tp", None) or model.tp
+    epilogue), down columns sharded (over every rank under component data parallelism of the
+    MLP, else over TP)."""
+    mg = model.comp_tp if getattr(model, "cdp_mlp", False) else model.tp
     W, r = mg.world, mg.rank
     g = shard_rows(get_tensor(p + "mlp.gate_proj.weight"), W, r)
     u = shard_rows(get_tensor(p + "mlp.up_proj.weight"), W, r)
