@@ -22,9 +22,10 @@ def test_b200_config_accepts_reference_keys():
         B200Config.from_dict({"attention_dp_size": 0})
     with pytest.raises(ValueError):
         B200Config.from_dict({"quantization": "int3"})
+    # component / attention DP sizes are accepted (checked against the replicas by the front end)
+    assert B200Config.from_dict({"mlp_dp_size": 2, "lm_head_dp_size": 4}).lm_head_dp_size == 4
     # options of the reference that are not implemented are refused, not silently ignored
-    for bad in ({"mlp_dp_size": 2}, {"embedding_dp_size": 2}, {"lm_head_dp_size": 4},
-                {"fp8_packed_kv": True}, {"kv_segment_size_buckets": [512]},
+    for bad in ({"fp8_packed_kv": True}, {"kv_segment_size_buckets": [512]},
                 {"decode_context_length_buckets": [1024]}, {"on_device_sampling_config": None}):
         with pytest.raises(NotImplementedError):
             B200Config.from_dict(bad)
