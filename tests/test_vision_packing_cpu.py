@@ -137,3 +137,30 @@ def test_vision_config_keys():
     with pytest.raises(ValueError):
         VisionConfig.from_dict({"no_such_key": 1})
     assert VisionConfig.from_additional_config({"neuron_config": {}}) is None
+
+
+def test_mxfp8_vision_weights():
+    """Qwen3-VL vision linears (input widths in 128s) as MXFP8 weights: the encoder runs them
+    through the MXFP8 oracle on CPU and stays close to the bf16-weight encoder."""
+    from vllm_neuron_b200.models.qwen3_vl import Qwen3VLVision
+    from vllm_neuron_b200.ops import linear as L
+
+    vc = dict(hidden_size=128, intermediate_size=256, num_heads=2, depth=2, patch_size=8,
+              temporal_patch_size=2, spatial_merge_size=2, out_hidden_size=64,
+              num_position_embeddings=16, deepstack_visual_indexes=[0])
+    v = Qwen3VLVision(vc, torch.device("cpu"), torch.float32)
+    g = torch.Generator().manual_seed(4)
+    for p in v.parameters():
+        p.data.copy_(torch.randn(p.shape, generator=g) * 0.05)
+    grids = [(1, 4, 4), (1, 4, 8)]
+    pix = torch.randn(48, 3 * 2 * 64, generator=g)
+    ref, ref_d = v(pix, grids)
+
+    from vllm_neuron_b200.models.qwen3_vl import quantize_vision_mxfp8
+
+    n = quantize_vision_mxfp8(v)
+    assert isinstance(v.blocks[0].qkv_w, L.MXFP8Weight) and isinstance(v.patch_w, L.MXFP8Weight)
+    assert n == 1 + 2 * 4 + 2 * 2
+    got, got_d = v(pix, grids)
+    assert float((got - ref).norm() / ref.norm()) < 0.1
+    assert float((got_d - ref_d).norm() / ref_d.norm()) < 0.1

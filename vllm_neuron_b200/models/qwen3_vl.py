@@ -39,6 +39,9 @@ from .llama import LlamaForCausalLM
 
 
 def _lin(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None) -> torch.Tensor:
+    if isinstance(w, L.MXFP8Weight):  # MXFP8 vision weights (block-scaled tensor cores / oracle)
+        y = L.gemm_out(x.contiguous(), w) if x.shape[0] > 0 else x.new_zeros(0, w.shape[0])
+        return (y + b if b is not None else y).to(x.dtype)
     if x.is_cuda and x.dtype == torch.bfloat16 and x.shape[0] > 0:
         y = L.gemm_out(x.contiguous(), w)
     else:
@@ -203,7 +206,7 @@ class Qwen3VLVision(torch.nn.Module):
         ``[R, head_dim]``); ``attend(q, k, v)`` maps ``[R, heads, hd]`` bf16 tensors to the
         attention output ``[R, heads * hd]``.  Returns (merged ``[R / merge^2, out_hidden]``,
         DeepStack ``[n_deep, R / merge^2, out_hidden]``)."""
-        dt = self.patch_w.dtype
+        dt = self.patch_b.dtype
         H, nh = self.hidden, self.heads_l
         hd = H // self.heads
         deep = []
@@ -226,8 +229,8 @@ class Qwen3VLVision(torch.nn.Module):
 
     def _embed(self, pixels: torch.Tensor, grids: list[tuple[int, int, int]]):
         """Patch embedding + interpolated position table, and the rotary tables (flat rows)."""
-        dt = self.patch_w.dtype
-        x = _lin(pixels.to(self.patch_w.device, dt), self.patch_w, self.patch_b)
+        dt = self.patch_b.dtype
+        x = _lin(pixels.to(self.patch_b.device, dt), self.patch_w, self.patch_b)
         x = x + self._pos_embed(grids)
         cos, sin = self._rotary(grids)
         return x, cos, sin
@@ -280,6 +283,27 @@ class Qwen3VLVision(torch.nn.Module):
         emb, deep = (body or self.packed_body)(xp, cp, sp, mask)
         idx = VP.unpack_index(plan, self.merge ** 2).to(dev)
         return emb.index_select(0, idx), deep.index_select(1, idx)
+
+
+@torch.no_grad()
+def quantize_vision_mxfp8(v: "Qwen3VLVision") -> int:
+    """Turn the vision encoder's linear weights whose input width is a multiple of 128 (patch
+    embedding, block qkv / proj / fc1 / fc2, merger fc1 / fc2) into MXFP8 weights; returns how
+    many were converted."""
+    mods = [(v, ("patch_w",))] + [(blk, ("qkv_w", "proj_w", "fc1_w", "fc2_w")) for blk in v.blocks]
+    mods += [(m, ("fc1_w", "fc2_w")) for m in [v.merger, *v.deep_mergers]]
+    n = 0
+    for mod, names in mods:
+        for name in names:
+            w = getattr(mod, name)
+            if not isinstance(w, torch.Tensor) or w.dim() != 2 or w.shape[1] % 128:
+                continue
+            mw = L.MXFP8Weight.from_weight(w)
+            if name in mod._parameters:
+                del mod._parameters[name]
+            setattr(mod, name, mw)
+            n += 1
+    return n
 
 
 def mrope_positions(prompt: list[int], image_token_id, grids: list[tuple[int, int, int]],
@@ -375,7 +399,7 @@ class Qwen3VLForConditionalGeneration(LlamaForCausalLM):
         (graph, static inputs, static outputs)."""
         vis, dev = self.visual, self.device
         R, hd = nb * bs, vis.hidden // vis.heads
-        ins = (torch.zeros(R, vis.hidden, dtype=vis.patch_w.dtype, device=dev),
+        ins = (torch.zeros(R, vis.hidden, dtype=vis.patch_b.dtype, device=dev),
                torch.ones(R, hd, dtype=torch.float32, device=dev),
                torch.zeros(R, hd, dtype=torch.float32, device=dev),
                torch.ones(nb, 1, bs, bs, dtype=torch.bool, device=dev))
@@ -500,6 +524,17 @@ class Qwen3VLForConditionalGeneration(LlamaForCausalLM):
         deep_all = (torch.cat(d_parts).permute(1, 0, 2).contiguous() if nd
                     else emb_all.new_zeros(0, emb_all.shape[0], H))
         return emb_all, deep_all
+
+    @torch.no_grad()
+    def quantize_mxfp8(self) -> int:
+        """MXFP8 for the text decoder (see the Llama model) and for the vision encoder's linear
+        layers whose input width is a multiple of 128: patch embedding, every block's qkv /
+        proj / fc1 / fc2 and the mergers' fc1 / fc2 (vision TP shards are quantized as
+        loaded).  Reference: the MXFP8 Qwen3-VL (vllm_neuron/model/qwen3_vl/model_mxfp8.py,
+        weight_loaders_mxfp8.py)."""
+        n = super().quantize_mxfp8() + quantize_vision_mxfp8(self.visual)
+        self.mx_linears = n
+        return n
 
     def load_hf_state_dict(self, get_tensor, names: set[str]):
         from ..utils.weight_loader import load_dense_decoder, load_qwen3_vl_vision
