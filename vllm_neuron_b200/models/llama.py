@@ -251,6 +251,9 @@ class LlamaForCausalLM(torch.nn.Module):
         sc = getattr(self, "kv_scales", None)
         return sc[kv_layer] if sc else (1.0, 1.0)
 
+    # decoders whose forward and checkpoint layout the component / attention DP paths cover
+    supports_component_dp = True
+
     # weights that block-FP8 serving quantizes (2-D linears, 3-D expert stacks); the router,
     # norms, embeddings and LM head stay bf16
     BLOCK_FP8_PARAMS = ("qkv", "o", "gate_up", "down", "w_gu", "w_down", "sh_gu", "sh_down",
@@ -586,8 +589,10 @@ class LlamaForCausalLM(torch.nn.Module):
         Reference: component-level DP sharding (``mlp_dp_size`` / ``embedding_dp_size`` /
         ``lm_head_dp_size``, docs/design/parallelism/component_dp_sharding.md; groups
         vllm_neuron/parallel/neuron_parallel_state.py:619-665)."""
-        if type(self)._mlp is not LlamaForCausalLM._mlp or type(self).load_hf_state_dict is not LlamaForCausalLM.load_hf_state_dict:
-            raise NotImplementedError(f"component data parallelism: {type(self).__name__} is not a dense decoder")
+        if type(self).forward is not LlamaForCausalLM.forward or not getattr(self, "supports_component_dp", False):
+            raise NotImplementedError(f"component data parallelism: {type(self).__name__} is not supported")
+        if mlp and type(self)._mlp is not LlamaForCausalLM._mlp:
+            raise NotImplementedError(f"mlp_dp_size: {type(self).__name__} has no dense MLP (experts use EP)")
         W = comp_tp.world
         p = lambda *s: torch.nn.Parameter(torch.empty(*s, dtype=self.dtype, device=self.device), requires_grad=False)
         self.dpcol, self.comp_tp = dpcol, comp_tp

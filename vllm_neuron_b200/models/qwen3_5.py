@@ -40,6 +40,7 @@ def num_state_slots(max_seqs: int) -> int:
 
 
 class Qwen3_5MoeForCausalLM(Qwen3MoeForCausalLM):
+    supports_component_dp = False  # own checkpoint layout / forward
     supports_dcp = False  # sinks / sliding windows / linear-attention state
     supports_prefix_caching = False
 
