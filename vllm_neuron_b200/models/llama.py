@@ -645,10 +645,15 @@ class LlamaForCausalLM(torch.nn.Module):
             raise NotImplementedError("attention data parallelism with qkv biases")
         self.cdp_attn = True
         self.Hq_w = self.cfg.num_heads // W
+        # Q+K+V variant: with more KV heads than replica TP ranks, and a whole number of them per
+        # TP x DP rank, K / V are sharded and exchanged like Q (no replica holds another's K / V
+        # weights); otherwise K / V stay replica-TP (Q-only variant)
+        nkv, t = self.cfg.num_kv_heads, self.tp.world
+        self.Hkv_w = nkv // W if (nkv > t and nkv % W == 0) else 0
         p = lambda *s: torch.nn.Parameter(torch.empty(*s, dtype=self.dtype, device=self.device), requires_grad=False)
         for ly in self.layers:
-            ly.q_w = p(self.Hq_w * self.D, self.H)
-            ly.kv = p(2 * self.Hkv * self.D, self.H)
+            ly.q_w = p((self.Hq_w + 2 * self.Hkv_w) * self.D, self.H)
+            ly.kv = None if self.Hkv_w else p(2 * self.Hkv * self.D, self.H)
             ly.o = p(self.H, self.Hq_w * self.D)
             del ly.qkv
             ly.qkv = None
@@ -658,12 +663,18 @@ class LlamaForCausalLM(torch.nn.Module):
         ``x = post_norm(res += attention)`` for this replica's rows."""
         D, Tm, Dh = self.dpcol.world, max(self.dp_tmax, T, 1), self.D
         hw = self.Hq_w * Dh
+        kw = self.Hkv_w * Dh
         xall = self._gather_rows(x, T, Tm)
-        qw = L.gemm_out(xall, ly.q_w)                                     # [D * Tm, hw]
-        q_own = self.dpcol.all_to_all(qw.view(D, Tm, hw).contiguous())    # [source d, Tm, hw]
-        q_own = q_own.permute(1, 0, 2).reshape(Tm, D * hw)[:T]
-        kv = L.gemm_out(x[:T], ly.kv)
-        qkv = torch.cat([q_own, kv], dim=1).contiguous()
+        qw = L.gemm_out(xall, ly.q_w)                                     # [D * Tm, hw (+ 2 kw)]
+        own = self.dpcol.all_to_all(qw.view(D, Tm, hw + 2 * kw).contiguous())  # [source d, Tm, .]
+        own = own[:, :T]
+        q_own = own[..., :hw].permute(1, 0, 2).reshape(T, D * hw)
+        if self.Hkv_w:  # K and V heads of every source, in head order
+            k_own = own[..., hw:hw + kw].permute(1, 0, 2).reshape(T, D * kw)
+            v_own = own[..., hw + kw:].permute(1, 0, 2).reshape(T, D * kw)
+            qkv = torch.cat([q_own, k_own, v_own], dim=1).contiguous()
+        else:
+            qkv = torch.cat([q_own, L.gemm_out(x[:T], ly.kv)], dim=1).contiguous()
         q = self.ws_q[:T]
         ops.rope_kv_write(qkv, b.positions, self.cos_sin, self.Hq, self.Hkv, Dh, q, k_cache, v_cache,
                           b.slot_mapping, ly.q_norm, ly.k_norm, self.eps, rot_dim=self.cfg.rot_dim,

@@ -83,11 +83,16 @@ def load_dense_decoder(model, get_tensor: Callable[[str], torch.Tensor], names: 
         if getattr(model, "cdp_attn", False):
             # attention data parallelism: Q / O heads of this (replica, TP position) sub-group,
             # K / V of the replica's TP position
-            hq_w, dh = model.Hq_w, cfg.head_dim
+            hq_w, hk_w, dh = model.Hq_w, model.Hkv_w, cfg.head_dim
             h0 = r * (cfg.num_heads // W) + model.dpcol.rank * hq_w
-            _copy(ly.q_w, q[h0 * dh:(h0 + hq_w) * dh], p + "q_proj")
-            kv = fused_qkv(q, k, v, cfg.num_heads, cfg.num_kv_heads, dh, W, r)[model.Hq * dh:]
-            _copy(ly.kv, kv, p + "kv")
+            qs = q[h0 * dh:(h0 + hq_w) * dh]
+            if hk_w:  # Q+K+V variant: this rank's K / V heads follow its Q heads
+                k0 = r * (cfg.num_kv_heads // W) + model.dpcol.rank * hk_w
+                qs = torch.cat([qs, k[k0 * dh:(k0 + hk_w) * dh], v[k0 * dh:(k0 + hk_w) * dh]], 0)
+            else:
+                kv = fused_qkv(q, k, v, cfg.num_heads, cfg.num_kv_heads, dh, W, r)[model.Hq * dh:]
+                _copy(ly.kv, kv, p + "kv")
+            _copy(ly.q_w, qs, p + "q_proj")
             _copy(ly.o, get_tensor(p + "self_attn.o_proj.weight")[:, h0 * dh:(h0 + hq_w) * dh], p + "o_proj")
             if ly.q_norm is not None:
                 _copy(ly.q_norm, get_tensor(p + "self_attn.q_norm.weight"), p + "q_norm")
