@@ -17,7 +17,10 @@ ALL = {"mlp_dp_size": 2, "embedding_dp_size": 2, "lm_head_dp_size": 2}
 @pytest.mark.parametrize("world,tp,opts", [(2, 1, {"mlp_dp_size": 2}), (2, 1, ALL), (4, 2, ALL),
                                            (4, 2, {"lm_head_dp_size": 2}),
                                            (2, 1, {"attention_dp_size": 2}),
-                                           (4, 2, dict(ALL, attention_dp_size=2))])
+                                           (4, 2, dict(ALL, attention_dp_size=2)),
+                                           # four replicas, components shared by pairs or by all
+                                           (4, 1, {"mlp_dp_size": 2, "attention_dp_size": 4,
+                                                   "lm_head_dp_size": 2, "embedding_dp_size": 4})])
 def test_component_dp_matches_tp1(world, tp, opts):
     ckpt, _ = tiny_llama_checkpoint()
     prompts = random_prompts(n=5, length=20, seed=21)  # odd count: replicas get 3 and 2
@@ -46,7 +49,7 @@ def test_component_dp_matches_tp1(world, tp, opts):
 def test_component_dp_refusals():
     from vllm_neuron_b200.config import B200Config
 
-    with pytest.raises(NotImplementedError):
+    with pytest.raises(ValueError):
         from vllm_neuron_b200.entrypoints import LLM
 
         ckpt, _ = tiny_llama_checkpoint()

@@ -114,9 +114,9 @@ def build_model(args: EngineArgs, tp: GroupComm = SINGLE):
             raise ValueError(f"vision tp_size {vcfg.tp_size} does not match the vision TP group "
                              f"({model.visual.tp.world} ranks)")
         model.configure_vision(vcfg, cuda_graphs=b200_config.cuda_graphs)
-    cdp = {k: getattr(b200_config, k) > 1 for k in ("mlp_dp_size", "embedding_dp_size", "lm_head_dp_size",
-                                                    "attention_dp_size")}
-    if any(cdp.values()):
+    cdp = {k: getattr(b200_config, k) for k in ("mlp_dp_size", "embedding_dp_size", "lm_head_dp_size",
+                                                "attention_dp_size")}
+    if any(v > 1 for v in cdp.values()):
         # component / attention data parallelism (the front end made the replicas and the
         # TP x DP group): re-shard the components before the weights load; replicas step in
         # lockstep and run eagerly (their batch sizes differ per step)
@@ -127,9 +127,10 @@ def build_model(args: EngineArgs, tp: GroupComm = SINGLE):
             raise ValueError("component DP sizes must be passed to the LLM front end (no TP x DP group)")
         if not hasattr(model, "set_component_dp"):
             raise NotImplementedError(f"{type(model).__name__} does not support component data parallelism")
-        model.set_component_dp(st.dp, st.world, mlp=cdp["mlp_dp_size"], embed=cdp["embedding_dp_size"],
-                               lm_head=cdp["lm_head_dp_size"])
-        if cdp["attention_dp_size"]:
+        names = {"mlp_dp_size": "mlp", "embedding_dp_size": "embed", "lm_head_dp_size": "lm_head",
+                 "attention_dp_size": "attn"}
+        model.set_component_dp({names[k]: st.cdp[v] for k, v in cdp.items() if v > 1})
+        if cdp["attention_dp_size"] > 1:
             model.set_attention_dp()
         b200_config.cuda_graphs = False
         b200_config.sequence_parallel = False

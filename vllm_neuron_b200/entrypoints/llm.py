@@ -77,15 +77,13 @@ class LLM:
         cdp = {k: int(opts.get(k, 1) or 1) for k in ("embedding_dp_size", "mlp_dp_size", "lm_head_dp_size",
                                                       "attention_dp_size")}
         for k, v in cdp.items():
-            if v > 1 and v != dp:
-                raise NotImplementedError(f"{k}={v}: component data parallelism spans every data-parallel "
-                                          f"replica ({k} = data_parallel_size = {dp})")
+            if v > 1 and dp % v:
+                raise ValueError(f"{k}={v} must divide the data-parallel size ({dp})")
         st = ps.initialize_parallel_state(ps.ParallelConfig(world_size=world,
                                                             tensor_parallel_size=tensor_parallel_size,
                                                             data_parallel_size=dp,
                                                             decode_context_parallel_size=decode_context_parallel_size,
-                                                            component_dp=any(v > 1 for v in cdp.values()),
-                                                            attention_dp_size=cdp["attention_dp_size"],
+                                                            component_dp_sizes=tuple(v for v in cdp.values() if v > 1),
                                                             vision_tp_size=vision_tp_of(additional_config)))
         # Data parallelism: each group of TP ranks is an independent engine replica serving
         # every dp-th request; outputs are gathered over the DP group (reference: data

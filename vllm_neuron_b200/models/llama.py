@@ -575,14 +575,15 @@ class LlamaForCausalLM(torch.nn.Module):
             h = L.gemm_out(act, ly.down, out=self.ws_h[:T])
             self._reduce_norm(h, res, nxt_norm, x)
 
-    def set_component_dp(self, dpcol: GroupComm, comp_tp: GroupComm, mlp: bool = False,
-                         embed: bool = False, lm_head: bool = False):
+    def set_component_dp(self, groups: dict):
         """Component data parallelism over data-parallel replicas that step in lockstep: the
         chosen components (dense MLP, embedding, LM head) shard their weights over ``comp_tp``
         (every rank of every replica, TP x DP) instead of the replica's TP group.  Before such a
         component, the replicas' rows are all-gathered over ``dpcol`` (the ranks at this TP
         position in the other replicas), padded to the step's largest replica batch
         (``dp_tmax`` tokens / ``dp_smax`` logits rows); each rank computes its shard on all rows,
+        ``groups`` maps each component (``"mlp"``, ``"embed"``, ``"lm_head"``, ``"attn"``) to its
+        (DP column, component TP group): k replicas share a component when its size is k;
         the shards are combined over ``comp_tp`` (all-reduce, or an all-gather of vocab slices
         for the LM head) and each replica keeps its own rows.  Attention (and its KV cache of
         the replica's own requests) stays on the replica.  Call before the weights load.
@@ -591,13 +592,15 @@ class LlamaForCausalLM(torch.nn.Module):
         vllm_neuron/parallel/neuron_parallel_state.py:619-665)."""
         if type(self).forward is not LlamaForCausalLM.forward or not getattr(self, "supports_component_dp", False):
             raise NotImplementedError(f"component data parallelism: {type(self).__name__} is not supported")
-        if mlp and type(self)._mlp is not LlamaForCausalLM._mlp:
+        if "mlp" in groups and type(self)._mlp is not LlamaForCausalLM._mlp:
             raise NotImplementedError(f"mlp_dp_size: {type(self).__name__} has no dense MLP (experts use EP)")
-        W = comp_tp.world
         p = lambda *s: torch.nn.Parameter(torch.empty(*s, dtype=self.dtype, device=self.device), requires_grad=False)
-        self.dpcol, self.comp_tp = dpcol, comp_tp
+        self.cdp_groups = dict(groups)
+        self.dpcol, self.comp_tp = next(iter(groups.values()))  # any: marks lockstep stepping
+        mlp, embed, lm_head = ("mlp" in groups), ("embed" in groups), ("lm_head" in groups)
         tied = self.lm_head is self.embed
         if mlp:
+            W = groups["mlp"][1].world
             if self.cfg.intermediate_size % W:
                 raise ValueError(f"the MLP width {self.cfg.intermediate_size} does not split over {W} ranks")
             self.cdp_mlp = True
@@ -607,12 +610,14 @@ class LlamaForCausalLM(torch.nn.Module):
                 self._make_mlp(ly, p, i)
             self.ws_act = torch.zeros(self.ws_act.shape[0], self.I, dtype=self.dtype, device=self.device)
             self.acc_gu = torch.zeros(self.acc_gu.shape[0], 2 * self.I, dtype=torch.float32, device=self.device)
-        vl = math.ceil(self.V / W)
         if embed:
+            cg = groups["embed"][1]
+            vl = math.ceil(self.V / cg.world)
             self.cdp_embed = True
-            self.V_local_emb, self.vocab_start_emb = vl, comp_tp.rank * vl
+            self.V_local_emb, self.vocab_start_emb = vl, cg.rank * vl
             self.embed = p(vl, self.H)
         if lm_head:
+            vl = math.ceil(self.V / groups["lm_head"][1].world)
             self.cdp_lmh = True
             self.V_local_lmh = vl
             self.lm_head = p(vl, self.H)
@@ -636,9 +641,9 @@ class LlamaForCausalLM(torch.nn.Module):
         and each replica keeps its rows.  The K / V weights stay per replica (the reference's
         Q-only variant).  Reference: attention DP, docs/design/parallelism/attention_dp.md,
         vllm_neuron/model/llama3/model.py:341-408,1125-1157."""
-        if self.dpcol is None:
-            raise ValueError("attention data parallelism needs the component-DP groups (set_component_dp)")
-        W = self.comp_tp.world
+        if "attn" not in getattr(self, "cdp_groups", {}):
+            raise ValueError("attention data parallelism needs its groups (set_component_dp)")
+        W = self.cdp_groups["attn"][1].world
         if self.cfg.num_heads % W:
             raise ValueError(f"{self.cfg.num_heads} attention heads do not split over {W} ranks")
         if any(ly.qkv_bias is not None for ly in self.layers):
@@ -661,12 +666,13 @@ class LlamaForCausalLM(torch.nn.Module):
     def _attention_dp(self, ly, x, res, b: ForwardBatch, T: int, k_cache, v_cache, kv_scale):
         """One attention block under attention data parallelism (see set_attention_dp); leaves
         ``x = post_norm(res += attention)`` for this replica's rows."""
-        D, Tm, Dh = self.dpcol.world, max(self.dp_tmax, T, 1), self.D
+        dc, cg = self.cdp_groups["attn"]
+        D, Tm, Dh = dc.world, max(self.dp_tmax, T, 1), self.D
         hw = self.Hq_w * Dh
         kw = self.Hkv_w * Dh
-        xall = self._gather_rows(x, T, Tm)
+        xall = self._gather_rows(x, T, Tm, dc)
         qw = L.gemm_out(xall, ly.q_w)                                     # [D * Tm, hw (+ 2 kw)]
-        own = self.dpcol.all_to_all(qw.view(D, Tm, hw + 2 * kw).contiguous())  # [source d, Tm, .]
+        own = dc.all_to_all(qw.view(D, Tm, hw + 2 * kw).contiguous())  # [source d, Tm, .]
         own = own[:, :T]
         q_own = own[..., :hw].permute(1, 0, 2).reshape(T, D * hw)
         if self.Hkv_w:  # K and V heads of every source, in head order
@@ -684,31 +690,33 @@ class LlamaForCausalLM(torch.nn.Module):
         self._attention(q, attn, k_cache, v_cache, b, window=ly.window, sinks=ly.sinks, kv_scale=kv_scale)
         ap = attn.new_zeros(Tm, D, hw)
         ap[:T] = attn.view(T, D, hw)
-        arecv = self.dpcol.all_to_all(ap.permute(1, 0, 2).contiguous())   # [source replica, Tm, hw]
+        arecv = dc.all_to_all(ap.permute(1, 0, 2).contiguous())   # [source replica, Tm, hw]
         h = L.gemm_out(arecv.reshape(D * Tm, hw), ly.o)
-        self.comp_tp.all_reduce_(h)
-        r = self.dpcol.rank
+        cg.all_reduce_(h)
+        r = dc.rank
         self._add_norm_rows(h[r * Tm:r * Tm + T], res, ly.post_norm, x, T)
 
-    def _gather_rows(self, t: torch.Tensor, n: int, nmax: int) -> torch.Tensor:
-        """All replicas' first ``n`` rows of ``t`` (each padded to ``nmax``), replica-major."""
-        D = self.dpcol.world
+    def _gather_rows(self, t: torch.Tensor, n: int, nmax: int, dc: GroupComm) -> torch.Tensor:
+        """The DP column's replicas' first ``n`` rows of ``t`` (each padded to ``nmax``),
+        replica-major."""
+        D = dc.world
         tp_ = t.new_zeros((nmax,) + tuple(t.shape[1:]))
         tp_[:n] = t[:n]
-        return self.dpcol.all_gather(tp_.unsqueeze(0).contiguous(), dim=0).reshape((D * nmax,) + tuple(t.shape[1:]))
+        return dc.all_gather(tp_.unsqueeze(0).contiguous(), dim=0).reshape((D * nmax,) + tuple(t.shape[1:]))
 
     def _mlp_cdp(self, ly, x, res, nxt_norm, T: int):
         """Component-DP MLP: gather the replicas' rows, run this rank's MLP shard on all of
         them, all-reduce over every rank, keep this replica's rows."""
+        dc, cg = self.cdp_groups["mlp"]
         Tm = max(self.dp_tmax, T, 1)
-        xall = self._gather_rows(x, T, Tm)
+        xall = self._gather_rows(x, T, Tm, dc)
         if self.silu_blk:
             act = L.gemm_silu(xall, ly.gate_up)
         else:
             act = ops.silu_mul(L.gemm_out(xall, ly.gate_up))
         h = L.gemm_out(act, ly.down)
-        self.comp_tp.all_reduce_(h)
-        r = self.dpcol.rank
+        cg.all_reduce_(h)
+        r = dc.rank
         self._add_norm_rows(h[r * Tm:r * Tm + T], res, nxt_norm, x, T)
 
     def _embed_cdp(self, b: ForwardBatch, res: torch.Tensor, T: int):
@@ -717,22 +725,24 @@ class LlamaForCausalLM(torch.nn.Module):
         ids = b.input_ids[:T]
         if b.last_tok is not None:
             ids = torch.where(ids < 0, b.last_tok[(-ids - 1).clamp(min=0).long()].to(ids.dtype), ids)
+        dc, cg = self.cdp_groups["embed"]
         Tm = max(self.dp_tmax, T, 1)
-        iall = self._gather_rows(ids, T, Tm)
+        iall = self._gather_rows(ids, T, Tm, dc)
         e = ops.embedding(iall, self.embed, self.vocab_start_emb, self.vocab_start_emb + self.V_local_emb)
-        self.comp_tp.all_reduce_(e)
-        r = self.dpcol.rank
+        cg.all_reduce_(e)
+        r = dc.rank
         res.copy_(e[r * Tm:r * Tm + T])
 
     def _logits_cdp(self, xs: torch.Tensor) -> torch.Tensor:
         """Component-DP LM head: gather the replicas' logits rows, this rank's vocab slice for
         all of them, all-gather the slices over every rank, keep this replica's rows."""
         S = xs.shape[0]
+        dc, cg = self.cdp_groups["lm_head"]
         Sm = max(self.dp_smax, S, 1)
-        xall = self._gather_rows(xs, S, Sm)
+        xall = self._gather_rows(xs, S, Sm, dc)
         lg = L.gemm_out(xall, self.lm_head)
-        lg = self.comp_tp.all_gather(lg, dim=1)
-        r = self.dpcol.rank
+        lg = cg.all_gather(lg, dim=1)
+        r = dc.rank
         return lg[r * Sm:r * Sm + S, :self.V]
 
     def _add_norm_rows(self, h, res, norm_w, x, T: int):

@@ -85,7 +85,12 @@ class ParallelConfig:
     decode_context_parallel_size: int = 1
     attention_dp_size: int = 1
     vision_tp_size: int = 1
-    component_dp: bool = False   # embedding / MLP / LM head sharded over every rank
+    # component / attention DP sizes in use (k replicas share each such component)
+    component_dp_sizes: tuple = ()
+
+    @property
+    def component_dp(self) -> bool:
+        return bool(self.component_dp_sizes)
 
     def validate(self):
         if self.tensor_parallel_size * self.data_parallel_size != self.world_size:
@@ -94,10 +99,10 @@ class ParallelConfig:
             raise ValueError("DCP size must divide TP")
         if self.tensor_parallel_size % self.vision_tp_size:
             raise ValueError("vision_tp_size must divide TP")
-        if self.attention_dp_size > 1 and self.attention_dp_size != self.data_parallel_size:
-            raise ValueError("attention_dp_size must equal the data-parallel size")
-        if self.component_dp and self.data_parallel_size < 2:
-            raise ValueError("component data parallelism needs data-parallel replicas")
+        for k in self.component_dp_sizes:
+            if k < 2 or self.data_parallel_size % k:
+                raise ValueError(f"a component DP size of {k} must divide the data-parallel size "
+                                 f"({self.data_parallel_size})")
         ep = self.expert_parallel_size or self.world_size
         if self.world_size % ep:
             raise ValueError("EP size must divide the world size")
@@ -113,6 +118,8 @@ class ParallelState:
     dcp: GroupComm = field(default_factory=lambda: GroupComm(None))
     vision_tp: GroupComm = field(default_factory=lambda: GroupComm(None))
     world: GroupComm = field(default_factory=lambda: GroupComm(None))  # component DP: TP x DP ranks
+    # component DP size k -> (DP column of k replicas, TP x k component group) of this rank
+    cdp: dict = field(default_factory=dict)
     cpu: dist.ProcessGroup | None = None
     dp_cpu: dist.ProcessGroup | None = None   # gloo group of this rank's DP peers
     groups: dict = field(default_factory=dict)
@@ -176,8 +183,16 @@ def initialize_parallel_state(cfg: ParallelConfig) -> ParallelState:
         for g in tp_groups(W, tp):
             sets.extend(sub_groups(g, cfg.vision_tp_size)[0])
         st.vision_tp, _ = _make(sets, rank)
-    if cfg.component_dp:
-        st.world, _ = _make([list(range(W))], rank)
+    for k in sorted(set(cfg.component_dp_sizes)):
+        cols, comps = [], []
+        for g in range(W // tp // k):  # replicas [g k, (g + 1) k)
+            comps.append(list(range(g * k * tp, (g + 1) * k * tp)))
+            cols.extend([[(g * k + i) * tp + t for i in range(k)] for t in range(tp)])
+        dc, _ = _make(cols, rank)
+        cg, _ = _make(comps, rank)
+        st.cdp[k] = (dc, cg)
+        if k == W // tp:
+            st.world = cg
     st.cpu = dist.new_group(list(range(W)), backend="gloo")
     if W // tp > 1:
         for g in dp_groups(W, tp):

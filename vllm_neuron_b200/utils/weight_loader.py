@@ -67,10 +67,11 @@ def load_dense_decoder(model, get_tensor: Callable[[str], torch.Tensor], names: 
     if any(n.startswith("model.language_model.") for n in names):
         pre = "model.language_model."
     # component data parallelism shards the embedding / LM head over every rank
-    cg = getattr(model, "comp_tp", None)
-    ew, er, ev = ((cg.world, cg.rank, model.V_local_emb) if getattr(model, "cdp_embed", False)
+    grp = getattr(model, "cdp_groups", {})
+    eg, hg = grp.get("embed", (None, None))[1], grp.get("lm_head", (None, None))[1]
+    ew, er, ev = ((eg.world, eg.rank, model.V_local_emb) if getattr(model, "cdp_embed", False)
                   else (W, r, model.V_local))
-    hw, hr, hv = ((cg.world, cg.rank, model.V_local_lmh) if getattr(model, "cdp_lmh", False)
+    hw, hr, hv = ((hg.world, hg.rank, model.V_local_lmh) if getattr(model, "cdp_lmh", False)
                   else (W, r, model.V_local))
     _copy(model.embed, shard_rows(get_tensor(pre + "embed_tokens.weight"), ew, er, ev), "embed")
     for i, ly in enumerate(model.layers):
@@ -84,10 +85,11 @@ def load_dense_decoder(model, get_tensor: Callable[[str], torch.Tensor], names: 
             # attention data parallelism: Q / O heads of this (replica, TP position) sub-group,
             # K / V of the replica's TP position
             hq_w, hk_w, dh = model.Hq_w, model.Hkv_w, cfg.head_dim
-            h0 = r * (cfg.num_heads // W) + model.dpcol.rank * hq_w
+            d = model.cdp_groups["attn"][0].rank
+            h0 = r * (cfg.num_heads // W) + d * hq_w
             qs = q[h0 * dh:(h0 + hq_w) * dh]
             if hk_w:  # Q+K+V variant: this rank's K / V heads follow its Q heads
-                k0 = r * (cfg.num_kv_heads // W) + model.dpcol.rank * hk_w
+                k0 = r * (cfg.num_kv_heads // W) + d * hk_w
                 qs = torch.cat([qs, k[k0 * dh:(k0 + hk_w) * dh], v[k0 * dh:(k0 + hk_w) * dh]], 0)
             else:
                 kv = fused_qkv(q, k, v, cfg.num_heads, cfg.num_kv_heads, dh, W, r)[model.Hq * dh:]
@@ -131,7 +133,7 @@ def load_dense_mlp(model, ly, get_tensor, p: str):
     """SwiGLU MLP of one layer: gate/up rows sharded (and block-interleaved for the fused SiLU
     epilogue), down columns sharded (over every rank under component data parallelism of the
     MLP, else over TP)."""
-    mg = model.comp_tp if getattr(model, "cdp_mlp", False) else model.tp
+    mg = model.cdp_groups["mlp"][1] if getattr(model, "cdp_mlp", False) else model.tp
     W, r = mg.world, mg.rank
     g = shard_rows(get_tensor(p + "mlp.gate_proj.weight"), W, r)
     u = shard_rows(get_tensor(p + "mlp.up_proj.weight"), W, r)
