@@ -638,8 +638,9 @@ class LlamaForCausalLM(torch.nn.Module):
         heads of its TP position; K / V (replica TP, as before) and attention run on the
         replica's own KV cache; the reverse all-to-all hands each rank all replicas' attention
         rows for its heads, its O shard makes partial sums that are all-reduced over TP x DP,
-        and each replica keeps its rows.  The K / V weights stay per replica (the reference's
-        Q-only variant).  Reference: attention DP, docs/design/parallelism/attention_dp.md,
+        and each replica keeps its rows.  With more KV heads than TP ranks (a whole number per
+        TP x DP rank) K / V are sharded and exchanged with Q (Q+K+V variant), else they stay per
+        replica (Q-only variant).  DP here is the attention-DP size k (k replicas).  Reference: attention DP, docs/design/parallelism/attention_dp.md,
         vllm_neuron/model/llama3/model.py:341-408,1125-1157."""
         if "attn" not in getattr(self, "cdp_groups", {}):
             raise ValueError("attention data parallelism needs its groups (set_component_dp)")
