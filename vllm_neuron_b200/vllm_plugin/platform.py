@@ -163,6 +163,14 @@ class B200Platform(Platform):
             par.worker_cls = WORKER_CLS
         if par.pipeline_parallel_size != 1:
             raise ValueError("pipeline parallelism is not supported by the B200 platform")
+        # component / attention data parallelism needs replicas that step in lockstep, which the
+        # framework's own LLM front end drives; under vLLM's engine each DP replica steps alone
+        ac = dict(getattr(vllm_config, "additional_config", None) or {})
+        opts = ac.get("neuron_config") or ac.get("b200_config") or {}
+        for key in ("attention_dp_size", "mlp_dp_size", "embedding_dp_size", "lm_head_dp_size"):
+            if int(opts.get(key, 1) or 1) > 1:
+                raise ValueError(f"{key} > 1 is served by vllm_neuron_b200.entrypoints.LLM (lockstep "
+                                 "replicas); the vLLM plugin runs independent data-parallel replicas")
         if par.distributed_executor_backend not in ("mp", "uni"):
             par.distributed_executor_backend = "uni" if par.world_size == 1 else "mp"
         # vLLM's asynchronous scheduling is served: the worker launches each step with the
