@@ -86,3 +86,32 @@ def test_attention_dp_on_moe_model():
         assert not isinstance(res[r], str), res[r]
         # the worker generates 8 tokens; compare the first 6
         assert [t[:6] for t in res[r][0]] == ref, (r, res[r][0], ref)
+
+
+def test_attention_dp_on_gpt_oss():
+    """GPT-OSS (qkv and o biases, sinks, sliding windows) with attention / embedding / LM-head
+    DP over two replicas equals the single-process tokens."""
+    from tests.test_gpt_oss_cpu import _tiny_gpt_oss
+
+    ckpt, _ = _tiny_gpt_oss()
+    prompts = random_prompts(n=3, length=14, vocab=512, seed=6)
+    from vllm_neuron_b200.engine.sampling_params import SamplingParams
+    from vllm_neuron_b200.entrypoints import LLM
+
+    ref = LLM(ckpt, device="cpu", max_num_seqs=8, max_model_len=128, num_gpu_blocks=64,
+              max_num_batched_tokens=48).generate(prompts, SamplingParams(temperature=0, max_tokens=8, ignore_eos=True))
+    ref = [o.outputs[0].token_ids for o in ref]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    extra = {"additional_config": {"neuron_config": {"attention_dp_size": 2, "embedding_dp_size": 2,
+                                                     "lm_head_dp_size": 2}}}
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, ckpt, prompts, q, 1, extra)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    for r in range(2):
+        assert not isinstance(res[r], str), res[r]
+        assert res[r][0] == ref, (r, res[r][0], ref)

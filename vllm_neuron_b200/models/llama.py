@@ -647,8 +647,6 @@ class LlamaForCausalLM(torch.nn.Module):
         W = self.cdp_groups["attn"][1].world
         if self.cfg.num_heads % W:
             raise ValueError(f"{self.cfg.num_heads} attention heads do not split over {W} ranks")
-        if any(ly.qkv_bias is not None for ly in self.layers):
-            raise NotImplementedError("attention data parallelism with qkv biases")
         self.cdp_attn = True
         self.Hq_w = self.cfg.num_heads // W
         # Q+K+V variant: with more KV heads than replica TP ranks, and a whole number of them per
@@ -683,9 +681,12 @@ class LlamaForCausalLM(torch.nn.Module):
         else:
             qkv = torch.cat([q_own, L.gemm_out(x[:T], ly.kv)], dim=1).contiguous()
         q = self.ws_q[:T]
+        # (after the exchange the rows hold the replica TP position's heads in order: the
+        # replica-TP qkv bias applies as is)
         ops.rope_kv_write(qkv, b.positions, self.cos_sin, self.Hq, self.Hkv, Dh, q, k_cache, v_cache,
                           b.slot_mapping, ly.q_norm, ly.k_norm, self.eps, rot_dim=self.cfg.rot_dim,
-                          q_pos_scale=self.q_pos_scale, positions3=b.positions3,
+                          q_pos_scale=self.q_pos_scale, qkv_bias=self._f32(ly, "qkv_bias"),
+                          positions3=b.positions3,
                           mrope_section=self.mrope_section, k_scale=kv_scale[0], v_scale=kv_scale[1])
         attn = self.ws_attn[:T]
         self._attention(q, attn, k_cache, v_cache, b, window=ly.window, sinks=ly.sinks, kv_scale=kv_scale)
@@ -695,7 +696,10 @@ class LlamaForCausalLM(torch.nn.Module):
         h = L.gemm_out(arecv.reshape(D * Tm, hw), ly.o)
         cg.all_reduce_(h)
         r = dc.rank
-        self._add_norm_rows(h[r * Tm:r * Tm + T], res, ly.post_norm, x, T)
+        own = h[r * Tm:r * Tm + T]
+        if ly.o_bias is not None:
+            own = own + ly.o_bias
+        self._add_norm_rows(own, res, ly.post_norm, x, T)
 
     def _gather_rows(self, t: torch.Tensor, n: int, nmax: int, dc: GroupComm) -> torch.Tensor:
         """The DP column's replicas' first ``n`` rows of ``t`` (each padded to ``nmax``),

@@ -57,6 +57,33 @@ def _copy(dst: torch.nn.Parameter, src: torch.Tensor, name: str):
 
 
 @torch.no_grad()
+def _vocab_shards(model, W: int, r: int):
+    """(world, rank, rows) of the embedding and of the LM head: over the component group under
+    component data parallelism, else over TP."""
+    grp = getattr(model, "cdp_groups", {})
+    eg, hg = grp.get("embed", (None, None))[1], grp.get("lm_head", (None, None))[1]
+    e = (eg.world, eg.rank, model.V_local_emb) if getattr(model, "cdp_embed", False) else (W, r, model.V_local)
+    h = (hg.world, hg.rank, model.V_local_lmh) if getattr(model, "cdp_lmh", False) else (W, r, model.V_local)
+    return e, h
+
+
+def _load_attention_dp(model, ly, q, k, v, o, W: int, r: int, p: str):
+    """Attention data parallelism: Q / O heads of this (replica, TP position) sub-group; K / V
+    of the sub-group (Q+K+V variant) or of the replica's TP position (Q-only variant)."""
+    cfg = model.cfg
+    hq_w, hk_w, dh = model.Hq_w, model.Hkv_w, cfg.head_dim
+    d = model.cdp_groups["attn"][0].rank
+    h0 = r * (cfg.num_heads // W) + d * hq_w
+    qs = q[h0 * dh:(h0 + hq_w) * dh]
+    if hk_w:  # this rank's K / V heads follow its Q heads
+        k0 = r * (cfg.num_kv_heads // W) + d * hk_w
+        qs = torch.cat([qs, k[k0 * dh:(k0 + hk_w) * dh], v[k0 * dh:(k0 + hk_w) * dh]], 0)
+    else:
+        _copy(ly.kv, fused_qkv(q, k, v, cfg.num_heads, cfg.num_kv_heads, dh, W, r)[model.Hq * dh:], p + "kv")
+    _copy(ly.q_w, qs, p + "q_proj")
+    _copy(ly.o, o[:, h0 * dh:(h0 + hq_w) * dh], p + "o_proj")
+
+
 def load_dense_decoder(model, get_tensor: Callable[[str], torch.Tensor], names: set[str],
                        mlp_loader: Callable | None = None):
     """Llama/Qwen-style decoder; ``mlp_loader(model, layer, get_tensor, names, prefix)``
@@ -66,13 +93,8 @@ def load_dense_decoder(model, get_tensor: Callable[[str], torch.Tensor], names: 
     pre = "model." if any(n.startswith("model.") for n in names) else ""
     if any(n.startswith("model.language_model.") for n in names):
         pre = "model.language_model."
-    # component data parallelism shards the embedding / LM head over every rank
-    grp = getattr(model, "cdp_groups", {})
-    eg, hg = grp.get("embed", (None, None))[1], grp.get("lm_head", (None, None))[1]
-    ew, er, ev = ((eg.world, eg.rank, model.V_local_emb) if getattr(model, "cdp_embed", False)
-                  else (W, r, model.V_local))
-    hw, hr, hv = ((hg.world, hg.rank, model.V_local_lmh) if getattr(model, "cdp_lmh", False)
-                  else (W, r, model.V_local))
+    # component data parallelism shards the embedding / LM head over its group
+    (ew, er, ev), (hw, hr, hv) = _vocab_shards(model, W, r)
     _copy(model.embed, shard_rows(get_tensor(pre + "embed_tokens.weight"), ew, er, ev), "embed")
     for i, ly in enumerate(model.layers):
         p = f"{pre}layers.{i}."
@@ -82,20 +104,7 @@ def load_dense_decoder(model, get_tensor: Callable[[str], torch.Tensor], names: 
         k = get_tensor(p + "self_attn.k_proj.weight")
         v = get_tensor(p + "self_attn.v_proj.weight")
         if getattr(model, "cdp_attn", False):
-            # attention data parallelism: Q / O heads of this (replica, TP position) sub-group,
-            # K / V of the replica's TP position
-            hq_w, hk_w, dh = model.Hq_w, model.Hkv_w, cfg.head_dim
-            d = model.cdp_groups["attn"][0].rank
-            h0 = r * (cfg.num_heads // W) + d * hq_w
-            qs = q[h0 * dh:(h0 + hq_w) * dh]
-            if hk_w:  # Q+K+V variant: this rank's K / V heads follow its Q heads
-                k0 = r * (cfg.num_kv_heads // W) + d * hk_w
-                qs = torch.cat([qs, k[k0 * dh:(k0 + hk_w) * dh], v[k0 * dh:(k0 + hk_w) * dh]], 0)
-            else:
-                kv = fused_qkv(q, k, v, cfg.num_heads, cfg.num_kv_heads, dh, W, r)[model.Hq * dh:]
-                _copy(ly.kv, kv, p + "kv")
-            _copy(ly.q_w, qs, p + "q_proj")
-            _copy(ly.o, get_tensor(p + "self_attn.o_proj.weight")[:, h0 * dh:(h0 + hq_w) * dh], p + "o_proj")
+            _load_attention_dp(model, ly, q, k, v, get_tensor(p + "self_attn.o_proj.weight"), W, r, p)
             if ly.q_norm is not None:
                 _copy(ly.q_norm, get_tensor(p + "self_attn.q_norm.weight"), p + "q_norm")
                 _copy(ly.k_norm, get_tensor(p + "self_attn.k_norm.weight"), p + "k_norm")
@@ -161,7 +170,8 @@ def load_gpt_oss(model, get_tensor: Callable[[str], torch.Tensor], names: set[st
     cfg = model.cfg
     W, r = model.tp.world, model.tp.rank
     pre = "model."
-    _copy(model.embed, shard_rows(get_tensor(pre + "embed_tokens.weight"), W, r, model.V_local), "embed")
+    (ew, er, ev), (hw, hr, hv) = _vocab_shards(model, W, r)
+    _copy(model.embed, shard_rows(get_tensor(pre + "embed_tokens.weight"), ew, er, ev), "embed")
     e0, el = model.e_start, model.e_local
     for i, ly in enumerate(model.layers):
         p = f"{pre}layers.{i}."
@@ -170,13 +180,16 @@ def load_gpt_oss(model, get_tensor: Callable[[str], torch.Tensor], names: set[st
         q = get_tensor(p + "self_attn.q_proj.weight")
         k = get_tensor(p + "self_attn.k_proj.weight")
         v = get_tensor(p + "self_attn.v_proj.weight")
-        _copy(ly.qkv, fused_qkv(q, k, v, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, W, r), p + "qkv")
+        if getattr(model, "cdp_attn", False):
+            _load_attention_dp(model, ly, q, k, v, get_tensor(p + "self_attn.o_proj.weight"), W, r, p)
+        else:
+            _copy(ly.qkv, fused_qkv(q, k, v, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, W, r), p + "qkv")
+            _copy(ly.o, shard_cols(get_tensor(p + "self_attn.o_proj.weight"), W, r), p + "o_proj")
         qb = get_tensor(p + "self_attn.q_proj.bias")[:, None]
         kb = get_tensor(p + "self_attn.k_proj.bias")[:, None]
         vb = get_tensor(p + "self_attn.v_proj.bias")[:, None]
         _copy(ly.qkv_bias, fused_qkv(qb, kb, vb, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, W, r)[:, 0],
               p + "qkv_bias")
-        _copy(ly.o, shard_cols(get_tensor(p + "self_attn.o_proj.weight"), W, r), p + "o_proj")
         _copy(ly.o_bias, get_tensor(p + "self_attn.o_proj.bias"), p + "o_proj.bias")
         sinks = get_tensor(p + "self_attn.sinks").float()
         _copy(ly.sinks, sinks[r * model.Hq:(r + 1) * model.Hq], p + "sinks")
@@ -207,7 +220,7 @@ def load_gpt_oss(model, get_tensor: Callable[[str], torch.Tensor], names: set[st
                                        get_tensor(dn_name + "_blocks")[e0:e0 + el],
                                        get_tensor(dn_name + "_scales")[e0:e0 + el])
     _copy(model.final_norm, get_tensor(pre + "norm.weight"), "norm")
-    _copy(model.lm_head, shard_rows(get_tensor("lm_head.weight"), W, r, model.V_local), "lm_head")
+    _copy(model.lm_head, shard_rows(get_tensor("lm_head.weight"), hw, hr, hv), "lm_head")
 
 
 @torch.no_grad()
