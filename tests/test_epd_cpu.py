@@ -196,3 +196,52 @@ def test_packed_vision_over_tp_ranks(vision):
     assert res[0][0] == ref and res[1][0] == ref, (res, ref)
     blocks = 3 if vision.get("tp_size", 1) == 2 else 2  # no DP replicas: no padding
     assert res[0][2] == blocks and res[1][2] == blocks
+
+
+def _cdp_vl_worker(rank, port, ckpt, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE="2",
+                      LOCAL_RANK=str(rank))
+    import torch
+
+    torch.set_num_threads(1)
+    from vllm_neuron_b200.engine.sampling_params import SamplingParams
+    from vllm_neuron_b200.entrypoints import LLM
+    from vllm_neuron_b200.parallel import state as ps
+
+    try:
+        llm = LLM(ckpt, tensor_parallel_size=1, **dict(KW, additional_config={"neuron_config": {
+            "attention_dp_size": 2, "embedding_dp_size": 2, "lm_head_dp_size": 2}}))
+        prompts = _three_image_prompts() * 2  # two image requests: one per replica
+        outs = llm.generate(prompts, SamplingParams(temperature=0, max_tokens=5, ignore_eos=True))
+        q.put((rank, [o.outputs[0].token_ids for o in outs]))
+    except Exception:  # pragma: no cover
+        import traceback
+
+        q.put((rank, traceback.format_exc()))
+    finally:
+        ps.destroy_parallel_state()
+
+
+def test_component_dp_vision_language():
+    """Qwen3-VL with attention / embedding / LM-head DP over two replicas (each encodes its own
+    requests' images; image rows replace the gathered embedding on the replica): tokens equal
+    the single-process run."""
+    from vllm_neuron_b200.engine.sampling_params import SamplingParams
+    from vllm_neuron_b200.entrypoints import LLM
+
+    d, _ = _ckpt()
+    prompts = _three_image_prompts() * 2
+    ref = LLM(d, **KW).generate(prompts, SamplingParams(temperature=0, max_tokens=5, ignore_eos=True))
+    ref = [o.outputs[0].token_ids for o in ref]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_cdp_vl_worker, args=(r, port, d, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    for r in (0, 1):
+        assert not isinstance(res[r], str), res[r]
+        assert res[r] == ref, (res, ref)
