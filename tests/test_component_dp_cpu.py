@@ -115,3 +115,36 @@ def test_attention_dp_on_gpt_oss():
     for r in range(2):
         assert not isinstance(res[r], str), res[r]
         assert res[r][0] == ref, (r, res[r][0], ref)
+
+
+def test_vocab_dp_on_hybrid_and_refusal():
+    """Embedding / LM-head DP on the Qwen3.5/3.6-style hybrid (DeltaNet and gated attention stay
+    per replica) equals the single-process tokens; attention DP is refused for it."""
+    from tests.test_hybrid_cpu import _tiny_hybrid
+
+    d, _ = _tiny_hybrid()
+    prompts = random_prompts(n=3, length=12, vocab=512, seed=8)
+    from vllm_neuron_b200.engine.sampling_params import SamplingParams
+    from vllm_neuron_b200.entrypoints import LLM
+
+    kw = dict(device="cpu", dtype="float32", max_num_seqs=8, max_model_len=128, num_gpu_blocks=64,
+              max_num_batched_tokens=48)
+    ref = LLM(d, **kw).generate(prompts, SamplingParams(temperature=0, max_tokens=8, ignore_eos=True))
+    ref = [o.outputs[0].token_ids for o in ref]
+    ctx = mp.get_context("spawn")
+    for opts, ok in (({"embedding_dp_size": 2, "lm_head_dp_size": 2}, True), ({"attention_dp_size": 2}, False)):
+        q = ctx.Queue()
+        port = _free_port()
+        extra = {"dtype": "float32", "additional_config": {"neuron_config": opts}}
+        procs = [ctx.Process(target=_worker, args=(r, 2, port, d, prompts, q, 1, extra)) for r in range(2)]
+        for p in procs:
+            p.start()
+        res = dict(q.get(timeout=300) for _ in procs)
+        for p in procs:
+            p.join(timeout=60)
+        for r in range(2):
+            if ok:
+                assert not isinstance(res[r], str), res[r]
+                assert res[r][0] == ref, (r, res[r][0], ref)
+            else:
+                assert isinstance(res[r], str) and "not supported" in res[r], res[r]

@@ -68,7 +68,6 @@ def _quant_experts(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
 
 
 class GptOssForCausalLM(MoEMixin, LlamaForCausalLM):
-    supports_component_dp = True  # attention / embedding / LM head (experts use EP)
     supports_dcp = False  # sinks / sliding windows / linear-attention state
     route_mode = M.ROUTE_TOPK_SOFTMAX
     expert_act = M.ACT_GPTOSS

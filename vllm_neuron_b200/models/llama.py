@@ -251,8 +251,8 @@ class LlamaForCausalLM(torch.nn.Module):
         sc = getattr(self, "kv_scales", None)
         return sc[kv_layer] if sc else (1.0, 1.0)
 
-    # decoders whose forward and checkpoint layout the component / attention DP paths cover
-    supports_component_dp = True
+    # components whose component / attention DP this model's forward and checkpoint loader cover
+    component_dp_parts = ("mlp", "embed", "lm_head", "attn")
 
     # weights that block-FP8 serving quantizes (2-D linears, 3-D expert stacks); the router,
     # norms, embeddings and LM head stay bf16
@@ -590,10 +590,12 @@ class LlamaForCausalLM(torch.nn.Module):
         Reference: component-level DP sharding (``mlp_dp_size`` / ``embedding_dp_size`` /
         ``lm_head_dp_size``, docs/design/parallelism/component_dp_sharding.md; groups
         vllm_neuron/parallel/neuron_parallel_state.py:619-665)."""
-        if type(self).forward is not LlamaForCausalLM.forward or not getattr(self, "supports_component_dp", False):
-            raise NotImplementedError(f"component data parallelism: {type(self).__name__} is not supported")
-        if "mlp" in groups and type(self)._mlp is not LlamaForCausalLM._mlp:
-            raise NotImplementedError(f"mlp_dp_size: {type(self).__name__} has no dense MLP (experts use EP)")
+        parts = set(self.component_dp_parts)
+        if type(self)._mlp is not LlamaForCausalLM._mlp:
+            parts.discard("mlp")  # expert MLPs shard by EP instead
+        bad = sorted(set(groups) - parts)
+        if bad:
+            raise NotImplementedError(f"component data parallelism of {bad} is not supported by {type(self).__name__}")
         p = lambda *s: torch.nn.Parameter(torch.empty(*s, dtype=self.dtype, device=self.device), requires_grad=False)
         self.cdp_groups = dict(groups)
         self.dpcol, self.comp_tp = next(iter(groups.values()))  # any: marks lockstep stepping

@@ -40,7 +40,7 @@ def num_state_slots(max_seqs: int) -> int:
 
 
 class Qwen3_5MoeForCausalLM(Qwen3MoeForCausalLM):
-    supports_component_dp = False  # own checkpoint layout / forward
+    component_dp_parts = ("embed", "lm_head")  # gated attention / DeltaNet stay per replica
     supports_dcp = False  # sinks / sliding windows / linear-attention state
     supports_prefix_caching = False
 
@@ -121,9 +121,12 @@ class Qwen3_5MoeForCausalLM(Qwen3MoeForCausalLM):
         tp = self.tp
         res = self.ws_residual[:T]
         x = self.ws_x[:T]
-        ops.embedding(b.input_ids, self.embed, self.vocab_start, self.vocab_start + self.V_local, out=res,
-                      last_tok=b.last_tok)
-        tp.all_reduce_(res)
+        if self.cdp_embed:
+            self._embed_cdp(b, res, T)
+        else:
+            ops.embedding(b.input_ids, self.embed, self.vocab_start, self.vocab_start + self.V_local, out=res,
+                          last_tok=b.last_tok)
+            tp.all_reduce_(res)
         ops.rmsnorm(res, self.layers[0].input_norm, self.eps, out=x)
         cs = self.capture
         if cs is not None and cs.point("model.embed_tokens", res):

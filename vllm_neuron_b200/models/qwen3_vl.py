@@ -340,7 +340,6 @@ def mrope_positions(prompt: list[int], image_token_id, grids: list[tuple[int, in
 
 class Qwen3VLForConditionalGeneration(LlamaForCausalLM):
     supports_prefix_caching = False  # image tokens share ids: cached blocks would not match pixels
-    supports_component_dp = True     # image rows / DeepStack features stay per replica
 
     def __init__(self, cfg, *args, **kw):
         super().__init__(cfg, *args, **kw)

@@ -234,7 +234,8 @@ def load_qwen3_5(model, get_tensor: Callable[[str], torch.Tensor], names: set[st
     W, r = model.tp.world, model.tp.rank
     pre = "model.language_model." if any(n.startswith("model.language_model.") for n in names) else "model."
     one = lambda t: t.float() + 1.0  # noqa: E731
-    _copy(model.embed, shard_rows(get_tensor(pre + "embed_tokens.weight"), W, r, model.V_local), "embed")
+    (ew, er, ev), (hw, hr, hv) = _vocab_shards(model, W, r)
+    _copy(model.embed, shard_rows(get_tensor(pre + "embed_tokens.weight"), ew, er, ev), "embed")
     Hk, Hv, dk, dv = model.lin_Hk, model.lin_Hv, model.lin_dk, model.lin_dv
     Kd, Vd = cfg.linear_num_key_heads * dk, cfg.linear_num_value_heads * dv
     for i, ly in enumerate(model.layers):
@@ -275,7 +276,7 @@ def load_qwen3_5(model, get_tensor: Callable[[str], torch.Tensor], names: set[st
     _copy(model.final_norm, one(get_tensor(pre + "norm.weight")), "norm")
     if cfg.tie_word_embeddings:
         return
-    _copy(model.lm_head, shard_rows(get_tensor("lm_head.weight"), W, r, model.V_local), "lm_head")
+    _copy(model.lm_head, shard_rows(get_tensor("lm_head.weight"), hw, hr, hv), "lm_head")
 
 
 _VIS_ATTR = {"attn.qkv.weight": "qkv_w", "attn.qkv.bias": "qkv_b", "attn.proj.weight": "proj_w",
